@@ -1,0 +1,74 @@
+/* tierstream B200 runtime: entry points beyond the reference ABI (include/strix_stream/ss.h). Plain pointers and
+ * sizes only. Device pointers are CUDA device addresses (or mapped pinned host addresses), streams are cudaStream_t
+ * passed as void* (NULL = the legacy default stream). Every function returns an ss_status; the message of a failure is
+ * in ss_last_error(). */
+#ifndef TIERSTREAM_TSB_H
+#define TIERSTREAM_TSB_H
+
+#include "../strix_stream/ss.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- K1 / K4 / K5: batched copies (the land kernel) ----
+ * n copies of bytes[i] bytes from src[i] to dst[i] in one launch (copies must not overlap each other; any side may be
+ * device memory, mapped pinned host memory or a peer device's memory). Then, when n_entries > 0, slot_of[keys[j]] =
+ * vals[j], and when ready_word is not NULL, *ready_word = ready_val, published once every copy landed. counter: one
+ * zeroed device word owned by the caller's stream (used and re-zeroed by the launch; NULL when nothing is published).
+ * At most 384 copies and 128 entries per call. Replaces, per miss, the reference's cudaMemcpyAsync per part plus a
+ * cuStreamWriteValue32 per entry and ready word (dg_ctx.cpp:163-216). */
+SS_API ss_status tsb_land(const void* const* src, void* const* dst, const uint64_t* bytes, uint32_t n,
+                          int32_t* slot_of, const uint32_t* keys, const int32_t* vals, uint32_t n_entries,
+                          uint32_t* ready_word, uint32_t ready_val, uint32_t* counter, uint32_t blocks, void* stream);
+
+/* ---- K3: device xxh64 of whole units ----
+ * Unit i is n_spans[i] (1..4) spans spans[4 i + s] of span_bytes[4 i + s] bytes hashed back to back (a gated unit's
+ * parts). units_dev: device scratch of n x 72 bytes (the unit table is staged there); out_dev: n hashes (device);
+ * expect_dev (may be NULL): n expected hashes, mismatches counted into *mismatches_dev (device word, not cleared).
+ * Bit-exact with the reference's host xxh64 (xxh64.cpp:39-112). */
+SS_API ss_status tsb_xxh64_units(const void* const* spans, const uint64_t* span_bytes, const uint32_t* n_spans,
+                                 uint32_t n, void* units_dev, const uint64_t* expect_dev, uint64_t* out_dev,
+                                 uint32_t* mismatches_dev, void* stream);
+
+/* ---- Deterministic replay of the device-gated slot cache on the host (test hook) ----
+ * The same configuration and outputs as the reference harness's replay: this library's slot cache (dg_core.cpp)
+ * driven in the service thread's order by a host mover whose events are complete when queried. tables: [tokens][keys]
+ * slot_of after each boundary; stats: [tokens][16] (tokens, lookups, misses, covered, fetched, prefetched,
+ * prefetch_used, resurrected, bank_serves, collected_mid, evicted, evict_short, writebacks_done, wb_deferred,
+ * wb_cancelled, wb_forced); read_sum (optional, with move_bytes and src_units): per (token, g, id) the checksum
+ * sum(byte * (pos % 251 + 1)) found through the table after the layer's demand. */
+typedef struct tsb_dg_replay_config {
+  uint32_t n_gated;
+  const uint32_t* n_units;
+  uint32_t n_parts;
+  const uint64_t* part_bytes;
+  uint32_t persistent_slots, bank_slots, blocks, spare_target;
+  uint32_t prefetch_reserve; /* 0xFFFFFFFF = auto */
+  uint32_t prefetch_per_layer, prefetch_per_token;
+  uint32_t wb_defer, wb_on_d2h;
+  uint64_t wb_layer_bytes, wb_max_outstanding;
+  uint32_t n_order;
+  const uint32_t* order;
+  uint32_t tokens, n_ids, n_pred;
+  uint32_t move_bytes;
+} tsb_dg_replay_config;
+SS_API ss_status tsb_test_dg_replay(const tsb_dg_replay_config* cfg, const int32_t* ids, const int32_t* preds,
+                                    int32_t* tables, uint64_t* stats, const uint8_t* src_units, uint64_t* read_sum);
+
+/* The device-gated context's slot table as the device holds it (cap >= the gated units; between tokens). Test hook:
+ * refused unless the context was opened with dg_test_hooks = 1. */
+SS_API ss_status tsb_test_dg_table(ss_ctx* c, int32_t* out, uint32_t cap);
+
+/* ---- Host xxh64 (this library's, the one the open's fill checks pinned units with; seed 0 in the descriptor) ---- */
+SS_API uint64_t tsb_xxh64(const void* data, size_t len, uint64_t seed);
+
+/* ---- Build facts ---- */
+/* 1000 x major + minor of the CUDA architecture the kernels were compiled for (100 for sm_100a). */
+SS_API int tsb_cuda_arch(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TIERSTREAM_TSB_H */

@@ -1,0 +1,73 @@
+"""TEST INFRASTRUCTURE ONLY: the CPU checkers the tests, __graft_entry__.smoke() and bench.py's cpu_baseline leg compare
+the product with. Nothing in tierstream_b200/ imports this package.
+
+  oracle/_ref/liboracle.so  the C restatement (oracle.c): xxh64, the synthetic bytes, the export mask, ss_dg_slot,
+                            the GPU tests' checksum; each function cites the reference file:line it restates.
+  oracle/_ref/libtsref.so   the reference's own C++ sources compiled directly (oracle/Makefile), with a harness
+                            (ref_harness.cpp) that replays a trace through the reference's DgCore.
+"""
+import ctypes as C
+import os
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+_orc = None
+_ref = None
+
+
+def orc():
+    global _orc
+    if _orc is None:
+        lib = C.CDLL(os.path.join(HERE, "_ref", "liboracle.so"))
+        lib.orc_xxh64.restype = C.c_uint64
+        lib.orc_xxh64.argtypes = [C.c_void_p, C.c_size_t, C.c_uint64]
+        lib.orc_xxh64_spans.restype = C.c_uint64
+        lib.orc_xxh64_spans.argtypes = [C.POINTER(C.c_void_p), C.POINTER(C.c_uint64), C.c_uint32, C.c_uint64]
+        lib.orc_fill_bytes.restype = None
+        lib.orc_fill_bytes.argtypes = [C.c_uint64, C.c_uint64, C.c_uint64, C.c_void_p]
+        lib.orc_checksum.restype = C.c_uint64
+        lib.orc_checksum.argtypes = [C.c_void_p, C.c_uint64]
+        lib.orc_export_mask.restype = C.c_uint64
+        lib.orc_export_mask.argtypes = [C.c_void_p, C.c_uint32, C.c_uint32, C.c_void_p, C.c_uint32,
+                                        C.POINTER(C.c_uint32)]
+        lib.orc_dg_slot.restype = C.c_int32
+        lib.orc_dg_slot.argtypes = [C.c_void_p, C.c_void_p, C.c_uint32, C.c_int32, C.c_uint32, C.c_uint32,
+                                    C.POINTER(C.c_uint32)]
+        _orc = lib
+    return _orc
+
+
+def ref_available():
+    return os.path.exists(os.path.join(HERE, "_ref", "libtsref.so"))
+
+
+def ref():
+    """The reference harness (None when oracle/_ref/libtsref.so was not built)."""
+    global _ref
+    if _ref is None and ref_available():
+        lib = C.CDLL(os.path.join(HERE, "_ref", "libtsref.so"))
+        lib.oref_xxh64.restype = C.c_uint64
+        lib.oref_xxh64.argtypes = [C.c_void_p, C.c_size_t, C.c_uint64]
+        lib.oref_dg_replay.restype = C.c_int
+        lib.oref_dg_replay.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
+                                       C.c_void_p, C.c_char_p, C.c_size_t]
+        _ref = lib
+    return _ref
+
+
+def ref_replay(cfg, ids, preds=None, src_units=None, want_reads=False):
+    """The reference DgCore's deterministic replay on the same config struct: (tables, stats[, read_sum])."""
+    import numpy as np
+    keys = sum(cfg.n_units[i] for i in range(cfg.n_gated))
+    ids = np.ascontiguousarray(ids, dtype=np.int32)
+    tables = np.empty((cfg.tokens, keys), dtype=np.int32)
+    stats = np.empty((cfg.tokens, 16), dtype=np.uint64)
+    reads = np.zeros((cfg.tokens, cfg.n_gated, cfg.n_ids), dtype=np.uint64) if want_reads else None
+    p = np.ascontiguousarray(preds, dtype=np.int32) if preds is not None else None
+    err = C.create_string_buffer(512)
+    rc = ref().oref_dg_replay(C.byref(cfg), ids.ctypes.data, p.ctypes.data if p is not None else None,
+                              tables.ctypes.data, stats.ctypes.data,
+                              src_units.ctypes.data if src_units is not None else None,
+                              reads.ctypes.data if reads is not None else None, err, 512)
+    if rc != 0:
+        raise RuntimeError("reference replay failed: " + err.value.decode())
+    return (tables, stats, reads) if want_reads else (tables, stats)

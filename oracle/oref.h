@@ -1,0 +1,47 @@
+/* C interface of the reference harness (oracle/_ref/libtsref.so, built by oracle/Makefile from the reference's own
+ * sources). TEST INFRASTRUCTURE ONLY: the tests, smoke() and bench.py's cpu_baseline leg use it as the checker; the
+ * product library never links or calls it. */
+#ifndef TSB_OREF_H
+#define TSB_OREF_H
+#include <stddef.h>
+#include <stdint.h>
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct oref_dg_config {
+  uint32_t n_gated;
+  const uint32_t* n_units;      /* [n_gated] */
+  uint32_t n_parts;
+  const uint64_t* part_bytes;   /* [n_parts] */
+  uint32_t persistent_slots, bank_slots, blocks, spare_target;
+  uint32_t prefetch_reserve;    /* 0xFFFFFFFF = auto, min(24, spare_target / 4) */
+  uint32_t prefetch_per_layer, prefetch_per_token;
+  uint32_t wb_defer, wb_on_d2h;
+  uint64_t wb_layer_bytes, wb_max_outstanding;
+  uint32_t n_order;
+  const uint32_t* order;        /* placement priority (keys) */
+  uint32_t tokens, n_ids, n_pred; /* ids: [tokens][n_gated][n_ids]; preds: [tokens][n_gated][n_pred] (for g + 1) */
+  uint32_t move_bytes;          /* 1 = the transport moves real bytes (host arena and blocks) */
+} oref_dg_config;
+
+/* Counters dumped per token (in this order). */
+#define OREF_NSTATS 16
+/* tokens, lookups, misses, covered, fetched, prefetched, prefetch_used, resurrected, bank_serves, collected_mid,
+ * evicted, evict_short, writebacks_done, wb_deferred, wb_cancelled, wb_forced */
+
+/* Replays the trace through the reference DgCore in the service thread's order with a host transport whose events are
+ * always complete. tables: [tokens][keys] slot_of after each boundary; stats: [tokens][OREF_NSTATS]. When move_bytes
+ * and src_units (keys x unit_bytes, each unit's bytes) are given, read_sum receives per (token, g, id) the checksum
+ * sum(byte * (pos % 251 + 1)) of the bytes found through the slot table after the layer's demand (0 for an absent
+ * entry). Returns 0, or -1 with the message in err. */
+int oref_dg_replay(const oref_dg_config* cfg, const int32_t* ids, const int32_t* preds, int32_t* tables,
+                   uint64_t* stats, const uint8_t* src_units, uint64_t* read_sum, char* err, size_t errlen);
+
+/* Reference xxh64 (the reference's own xxh64.cpp). */
+uint64_t oref_xxh64(const void* data, size_t len, uint64_t seed);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,155 @@
+// Reference harness (TEST INFRASTRUCTURE): drives the reference library's own DgCore, compiled from its sources, the
+// way its DgService::serve_token drives it (dg_service.cpp:269-365), with a host transport in the pattern of its
+// tests' immediate transport (tests/test_dg_service.cpp:33-85): every event complete when queried, copies done at
+// once. The product library never links this file.
+#include <cstdint>
+#include <cstdio>
+#include <cstring>
+#include <exception>
+#include <vector>
+
+#include "dg_core.hpp"
+#include "oref.h"
+#include "xxh64.hpp"
+
+namespace {
+
+class HostTransport final : public ts::DgTransport {
+ public:
+  HostTransport(const oref_dg_config& c, uint32_t keys, uint32_t slots)
+      : parts_(c.part_bytes, c.part_bytes + c.n_parts), table_(keys, -1), move_(c.move_bytes != 0) {
+    for (uint64_t b : parts_) unit_ += b;
+    if (move_) {
+      arena_.assign(size_t(slots) * unit_, 0);
+      blocks_.assign(size_t(c.blocks) * unit_, 0);
+      stage_.assign(unit_, 0);
+    }
+  }
+  uint8_t* slot_ptr(int32_t s) { return arena_.data() + size_t(s) * unit_; }
+  uint8_t* block_ptr(int32_t b) { return b < 0 ? stage_.data() : blocks_.data() + size_t(b) * unit_; }
+  void h2d(Stream, int32_t slot, int32_t block) override {
+    if (move_) std::memcpy(slot_ptr(slot), block_ptr(block), unit_);
+  }
+  void d2h(int32_t slot, int32_t block) override {
+    if (move_) std::memcpy(block_ptr(block), slot_ptr(slot), unit_);
+  }
+  void d2d(int32_t src, int32_t dst) override {
+    if (move_) std::memmove(slot_ptr(dst), slot_ptr(src), unit_);
+  }
+  void h2h(int32_t src, int32_t dst) override {
+    if (move_) std::memmove(block_ptr(dst), block_ptr(src), unit_);
+  }
+  void d2h_part(Stream, int32_t slot, int32_t block, uint32_t p) override {
+    if (!move_) return;
+    uint64_t off = 0;
+    for (uint32_t i = 0; i < p; ++i) off += parts_[i];
+    std::memcpy(block_ptr(block) + off, slot_ptr(slot) + off, parts_[p]);
+  }
+  uint32_t parts() const override { return uint32_t(parts_.size()); }
+  uint64_t part_bytes(uint32_t p) const override { return parts_[p]; }
+  void write_entry(Stream, uint32_t key, int32_t v) override { table_[key] = v; }
+  void signal_ready(uint32_t, uint32_t) override {}
+  void* event_create() override { return new int(0); }
+  void event_destroy(void* ev) override { delete static_cast<int*>(ev); }
+  void record(void*, Stream) override {}
+  void wait(Stream, void*) override {}
+  bool done(void*) override { return true; }
+  void event_sync(void*) override {}
+  void sync(Stream) override {}
+  void upload_table(const int32_t* t, uint32_t n) override { std::memcpy(table_.data(), t, size_t(n) * 4); }
+  void upload_table_ranges(const int32_t* t, const uint32_t* r, uint32_t n) override {
+    for (uint32_t i = 0; i < n; ++i) std::memcpy(table_.data() + r[2 * i], t + r[2 * i], size_t(r[2 * i + 1]) * 4);
+  }
+  std::vector<uint64_t> parts_;
+  std::vector<int32_t> table_;  // the "device" table the export rule reads
+  std::vector<uint8_t> arena_, blocks_, stage_;
+  uint64_t unit_ = 0;
+  bool move_;
+};
+
+uint64_t checksum(const uint8_t* p, uint64_t n) {
+  uint64_t s = 0;
+  for (uint64_t i = 0; i < n; ++i) s += uint64_t(p[i]) * (i % 251 + 1);
+  return s;
+}
+
+}  // namespace
+
+extern "C" __attribute__((visibility("default"))) uint64_t oref_xxh64(const void* data, size_t len, uint64_t seed) {
+  return ts::xxh64(data, len, seed);
+}
+
+extern "C" __attribute__((visibility("default"))) int oref_dg_replay(const oref_dg_config* c, const int32_t* ids,
+                                                                      const int32_t* preds, int32_t* tables,
+                                                                      uint64_t* stats, const uint8_t* src_units,
+                                                                      uint64_t* read_sum, char* err, size_t errlen) {
+  try {
+    ts::DgConfig cfg;
+    cfg.n_units.assign(c->n_units, c->n_units + c->n_gated);
+    cfg.persistent_slots = c->persistent_slots;
+    cfg.bank_slots = c->bank_slots;
+    cfg.blocks = c->blocks;
+    cfg.spare_target = c->spare_target;
+    cfg.prefetch_reserve_auto = c->prefetch_reserve == 0xFFFFFFFFu;
+    cfg.prefetch_reserve = cfg.prefetch_reserve_auto ? 0 : c->prefetch_reserve;
+    cfg.prefetch_per_layer = c->prefetch_per_layer;
+    cfg.prefetch_per_token = c->prefetch_per_token;
+    cfg.wb_defer = c->wb_defer != 0;
+    cfg.wb_on_d2h = c->wb_on_d2h != 0;
+    cfg.wb_layer_bytes = c->wb_layer_bytes;
+    cfg.wb_max_outstanding = c->wb_max_outstanding;
+    cfg.max_ids = c->n_ids ? c->n_ids : 1;
+    uint32_t keys = 0;
+    for (uint32_t g = 0; g < c->n_gated; ++g) keys += c->n_units[g];
+    const uint32_t slots = c->persistent_slots + 2 * c->bank_slots + 1;
+    HostTransport t(*c, keys, slots);
+    ts::DgCore core(cfg, &t);
+    std::vector<uint32_t> order(c->order, c->order + c->n_order);
+    for (uint32_t k = 0; k < keys; ++k) order.push_back(k);
+    core.place(order);
+    t.upload_table(core.table().data(), keys);
+    if (t.move_ && src_units)  // the open's fill: every unit into its slot or block
+      for (uint32_t k = 0; k < keys; ++k) {
+        uint8_t* dst = core.slot_of(k) >= 0 ? t.slot_ptr(core.slot_of(k)) : t.block_ptr(core.block_of(k));
+        std::memcpy(dst, src_units + size_t(k) * t.unit_, t.unit_);
+      }
+    std::vector<uint32_t> row(c->n_ids), pred(c->n_pred);
+    for (uint32_t tok = 0; tok < c->tokens; ++tok) {
+      core.begin_token(tok + 1);
+      for (uint32_t g = 0; g < c->n_gated; ++g) {
+        const int32_t* r = ids + (size_t(tok) * c->n_gated + g) * c->n_ids;
+        uint64_t mask = 0;
+        for (uint32_t i = 0; i < c->n_ids; ++i) {  // the export kernel's rule on the device table
+          row[i] = uint32_t(r[i]);
+          if (row[i] < c->n_units[g] && t.table_[core.key(g, row[i])] < 0) mask |= 1ull << i;
+        }
+        core.serve_demand(g, row.data(), c->n_ids, mask);
+        if (read_sum && t.move_)
+          for (uint32_t i = 0; i < c->n_ids; ++i) {
+            const int32_t s = t.table_[core.key(g, row[i])];
+            read_sum[(size_t(tok) * c->n_gated + g) * c->n_ids + i] = s < 0 ? 0 : checksum(t.slot_ptr(s), t.unit_);
+          }
+        core.serve_use(g, row.data(), c->n_ids, mask);
+        if (preds && c->n_pred && g + 1 < c->n_gated) {
+          const int32_t* p = preds + (size_t(tok) * c->n_gated + g) * c->n_pred;
+          for (uint32_t i = 0; i < c->n_pred; ++i) pred[i] = uint32_t(p[i]);
+          core.serve_prediction(g + 1, pred.data(), c->n_pred, c->n_ids, false);
+        }
+        if (core.deferred() && g + 1 < c->n_gated) core.issue_writebacks(g, [] { return false; });
+      }
+      core.end_token({});
+      std::memcpy(tables + size_t(tok) * keys, t.table_.data(), size_t(keys) * 4);
+      const ts::DgStats& s = core.stats();
+      const uint64_t v[OREF_NSTATS] = {s.tokens,          s.lookups,     s.misses,        s.covered,
+                                       s.fetched,         s.prefetched,  s.prefetch_used, s.resurrected,
+                                       s.bank_serves,     s.collected_mid, s.evicted,     s.evict_short,
+                                       s.writebacks_done, s.wb_deferred, s.wb_cancelled,  s.wb_forced};
+      std::memcpy(stats + size_t(tok) * OREF_NSTATS, v, sizeof v);
+      core.check();
+    }
+    return 0;
+  } catch (const std::exception& e) {
+    if (err && errlen) std::snprintf(err, errlen, "%s", e.what());
+    return -1;
+  }
+}

@@ -1,0 +1,729 @@
+// The C ABI (include/strix_stream/ss.h): every entry point catches, maps to ss_status and keeps the message per
+// thread; a device or allocation failure inside a context call poisons the context (the reference's rules,
+// capi.cpp:52-66 and 482-510 there). Functions outside this build's scope return SS_E_UNSUPPORTED.
+#include <algorithm>
+#include <cstdlib>
+#include <cstring>
+#include <fstream>
+#include <new>
+#include <sstream>
+
+#include "ctx.hpp"
+#include "desc.hpp"
+#include "errors.hpp"
+#include "json.hpp"
+#include "plan.hpp"
+#include "strix_stream/ss.h"
+#include "strix_stream/ss_test.h"
+#include "tierstream/tsb.h"
+
+struct ss_desc {
+  tsb::Desc d;
+};
+struct ss_plan {
+  tsb::Plan p;
+  const ss_desc* desc;
+};
+struct ss_ctx {
+  std::unique_ptr<tsb::HostContext> host;
+  std::unique_ptr<tsb::DgContext> dg;
+};
+
+namespace {
+
+thread_local std::string g_err;
+
+template <class F>
+ss_status guard(F&& f) {
+  try {
+    f();
+    return SS_OK;
+  } catch (const tsb::Error& e) {
+    g_err = e.what();
+    return e.status();
+  } catch (const std::bad_alloc&) {
+    g_err = "out of host memory";
+    return SS_E_NOMEM;
+  } catch (const std::exception& e) {
+    g_err = e.what();
+    return SS_E_BACKEND;
+  }
+}
+
+ss_status give_text(const std::string& s, char** out, size_t* len) {
+  if (!out) {
+    g_err = "null output pointer";
+    return SS_E_INVALID;
+  }
+  char* p = static_cast<char*>(std::malloc(s.size() + 1));
+  if (!p) {
+    g_err = "out of host memory";
+    return SS_E_NOMEM;
+  }
+  std::memcpy(p, s.data(), s.size());
+  p[s.size()] = 0;
+  *out = p;
+  if (len) *len = s.size();
+  return SS_OK;
+}
+
+void need(bool ok, const char* what) { tsb::require(ok, SS_E_INVALID, what); }
+
+ss_status unsupported(const char* fn) {
+  g_err = std::string(fn) + ": not in this build (the tierstream B200 runtime implements the weight-streaming hot "
+                            "path only)";
+  return SS_E_UNSUPPORTED;
+}
+
+void budget_defaults(ss_budget* b) {
+  std::memset(b, 0, sizeof *b);
+  b->struct_size = uint32_t(sizeof *b);
+  b->margin_gib = 2.0;
+  b->margin_fraction = 0.03;
+}
+
+void options_defaults(ss_options* o) {
+  std::memset(o, 0, sizeof *o);
+  o->struct_size = uint32_t(sizeof *o);
+  o->backend = SS_BACKEND_CUDA;  // the only backend of this build (the reference defaults to its CPU backend)
+  o->policy = SS_POLICY_LRU;
+  o->lookahead_budget = 2;
+  o->reader_threads = 2;
+  o->staging_buffers = 4;
+  o->staging_bytes = uint64_t(256) << 20;
+  o->copy_piece_bytes = uint64_t(64) << 20;
+  o->fill_residents = 1;
+  o->score_window = 16;
+  o->pin_planned = 1;
+  o->direct_io = 1;
+  o->forward_mode = SS_FORWARD_HOST;
+  o->dg_prefetch_reserve = 0xFFFFFFFFu;
+  o->dg_prefetch_per_layer = 4;
+  o->dg_prefetch_per_token = 48;
+  o->dg_wait_timeout_ms = 10000;
+  o->dg_spare_target = 0xFFFFFFFFu;
+  o->dg_wb_defer = 1;
+  o->dg_wb_stream = 1;
+  o->dg_score_w_trans = 700;
+  o->dg_score_w_freq = 200;
+  o->dg_score_w_recency = 100;
+  o->drive_readers = 4;
+}
+
+// Fills the first `size` bytes of *out with the defaults (struct_size = size).
+template <class T, class F>
+void sized_defaults(T* out, uint32_t size, F defaults) {
+  if (!out || size < sizeof(uint32_t)) return;
+  T full;
+  defaults(&full);
+  const size_t n = size < sizeof full ? size : sizeof full;
+  std::memcpy(out, &full, n);
+  out->struct_size = size;
+}
+
+// A versioned input struct: min(struct_size, own) bytes from the caller, the defaults for the rest.
+template <class T, class F>
+T versioned(const T* in, F defaults, const char* what) {
+  T v;
+  defaults(&v);
+  if (!in) return v;
+  tsb::require(in->struct_size >= sizeof(uint32_t), SS_E_INVALID, std::string(what) + ": struct_size not set");
+  const size_t n = in->struct_size < sizeof v ? in->struct_size : sizeof v;
+  std::memcpy(&v, in, n);
+  v.struct_size = uint32_t(sizeof v);
+  return v;
+}
+
+// A versioned output: the caller's size, at most ours.
+template <class T>
+void give_sized(T* out, uint32_t size, const T& full) {
+  const size_t n = size < sizeof full ? size : sizeof full;
+  std::memcpy(out, &full, n);
+  out->struct_size = uint32_t(n);
+}
+
+std::string read_text(const char* path) {
+  std::ifstream f(path, std::ios::binary);
+  tsb::require(bool(f), SS_E_IO, std::string("cannot open ") + path);
+  std::stringstream s;
+  s << f.rdbuf();
+  return s.str();
+}
+
+bool ctx_poisoned(const ss_ctx* c) { return c->dg ? c->dg->poisoned() : c->host->poisoned(); }
+void ctx_poison(ss_ctx* c) {
+  if (c->dg) c->dg->poison();
+  else c->host->poison();
+}
+tsb::HostContext& host_of(const ss_ctx* c, const char* fn) {
+  if (c->dg) tsb::fail(SS_E_INVALID, std::string(fn) + ": refused in device-gated mode");
+  return *c->host;
+}
+tsb::DgContext& dg_of(const ss_ctx* c, const char* fn) {
+  if (!c->dg) tsb::fail(SS_E_INVALID, std::string(fn) + ": the context is not device-gated");
+  return *c->dg;
+}
+
+// Context calls: a poisoned context refuses; a device, allocation or internal failure poisons.
+template <class F>
+ss_status ctx_guard(ss_ctx* c, F&& f) {
+  if (!c) {
+    g_err = "null context";
+    return SS_E_INVALID;
+  }
+  if (ctx_poisoned(c)) {
+    g_err = "context poisoned by an earlier device, out-of-memory or internal failure: close it";
+    return SS_E_BACKEND;
+  }
+  try {
+    f();
+    return SS_OK;
+  } catch (const tsb::Error& e) {
+    if (e.status() == SS_E_BACKEND || e.status() == SS_E_NOMEM) ctx_poison(c);
+    g_err = e.what();
+    return e.status();
+  } catch (const std::bad_alloc&) {
+    ctx_poison(c);
+    g_err = "out of host memory (context poisoned)";
+    return SS_E_NOMEM;
+  } catch (const std::exception& e) {
+    ctx_poison(c);
+    g_err = e.what();
+    return SS_E_BACKEND;
+  }
+}
+
+}  // namespace
+
+namespace tsb {
+const char* set_error(const std::string& msg) {
+  g_err = msg;
+  return g_err.c_str();
+}
+}  // namespace tsb
+
+extern "C" {
+
+const char* ss_last_error(void) { return g_err.c_str(); }
+int ss_abi_version(void) { return SS_ABI_VERSION; }
+
+// ---- descriptor ----
+ss_status ss_desc_from_json(const char* json_text, size_t len, ss_desc** out) {
+  return guard([&] {
+    need(json_text && out, "ss_desc_from_json: null argument");
+    *out = new ss_desc{tsb::desc_from_json(tsb::json_parse(std::string(json_text, len)))};
+  });
+}
+ss_status ss_desc_from_file(const char* path, ss_desc** out) {
+  return guard([&] {
+    need(path && out, "ss_desc_from_file: null argument");
+    *out = new ss_desc{tsb::desc_from_json(tsb::json_parse(read_text(path)))};
+  });
+}
+ss_status ss_desc_from_model(const char* manifest_path, ss_desc** out) { return ss_desc_from_file(manifest_path, out); }
+void ss_desc_free(ss_desc* d) { delete d; }
+int ss_desc_n_layers(const ss_desc* d) { return d ? int(d->d.layers.size()) : -1; }
+int ss_desc_layer_units(const ss_desc* d, int layer) {
+  if (!d || layer < 0 || size_t(layer) >= d->d.layers.size()) return -1;
+  return d->d.layers[size_t(layer)].n_units;
+}
+uint64_t ss_desc_unit_bytes(const ss_desc* d, int layer) {
+  if (!d || layer < 0 || size_t(layer) >= d->d.layers.size()) return 0;
+  return d->d.layers[size_t(layer)].unit_bytes;
+}
+ss_status ss_desc_to_json(const ss_desc* d, char** out_json, size_t* out_len) {
+  std::string s;
+  const ss_status st = guard([&] {
+    need(d != nullptr, "ss_desc_to_json: null descriptor");
+    s = tsb::json_write(tsb::desc_to_json(d->d));
+  });
+  return st != SS_OK ? st : give_text(s, out_json, out_len);
+}
+void ss_free(void* p) { std::free(p); }
+int64_t ss_desc_unit_index(const ss_desc* d, int layer, int unit) {
+  if (!d || layer < 0 || size_t(layer) >= d->d.layers.size()) return -1;
+  if (unit < 0 || unit >= d->d.layers[size_t(layer)].n_units) return -1;
+  return d->d.unit_base[size_t(layer)] + unit;
+}
+int64_t ss_desc_total_units(const ss_desc* d) { return d ? d->d.total_units : -1; }
+
+// ---- planner ----
+void ss_budget_defaults_sized(ss_budget* b, uint32_t size) { sized_defaults(b, size, budget_defaults); }
+ss_status ss_plan_make(const ss_desc* d, const ss_budget* b, const double* benefit, size_t n_benefit, ss_plan** out) {
+  return guard([&] {
+    need(d && b && out, "ss_plan_make: null argument");
+    need(!n_benefit || benefit, "ss_plan_make: null benefit");
+    ss_budget bb = versioned(b, budget_defaults, "ss_plan_make budget");
+    bb.reserved0 = 0;
+    std::vector<double> ben(benefit, benefit + n_benefit);
+    *out = new ss_plan{tsb::plan_make(d->d, bb, ben), d};
+  });
+}
+ss_status ss_plan_from_tiers(const ss_desc* d, const ss_budget* b, const uint8_t* tiers, size_t n, ss_plan** out) {
+  return guard([&] {
+    need(d && b && out && (tiers || !n), "ss_plan_from_tiers: null argument");
+    ss_budget bb = versioned(b, budget_defaults, "ss_plan_from_tiers budget");
+    bb.reserved0 = 0;
+    *out = new ss_plan{tsb::plan_from_tiers(d->d, bb, std::vector<uint8_t>(tiers, tiers + n)), d};
+  });
+}
+ss_status ss_plan_from_json(const ss_desc* d, const ss_budget* b, const char* plan_json, size_t len, ss_plan** out) {
+  return guard([&] {
+    need(d && b && plan_json && out, "ss_plan_from_json: null argument");
+    ss_budget bb = versioned(b, budget_defaults, "ss_plan_from_json budget");
+    bb.reserved0 = 0;
+    const tsb::Json j = tsb::json_parse(std::string(plan_json, len));
+    *out = new ss_plan{tsb::plan_from_tiers(d->d, bb, tsb::tiers_from_json(d->d, j)), d};
+  });
+}
+void ss_plan_free(ss_plan* p) { delete p; }
+ss_tier ss_plan_unit_tier(const ss_plan* p, int layer, int unit) {
+  const int64_t g = p ? ss_desc_unit_index(p->desc, layer, unit) : -1;
+  return g < 0 ? SS_TIER_DISK : ss_tier(p->p.tier[size_t(g)]);
+}
+void ss_plan_get_totals(const ss_plan* p, ss_plan_totals* out) {
+  if (!p || !out) return;
+  out->fixed_bytes = p->p.fixed;
+  out->margin_bytes = p->p.margin;
+  out->resident_bytes = p->p.resident;
+  out->dynamic_bytes = p->p.dynamic;
+  out->ring_bytes = p->p.ring;
+  out->peak_device_bytes = p->p.peak;
+  out->pinned_bytes = p->p.pinned;
+  out->disk_bytes = p->p.disk;
+  out->n_resident = p->p.n_resident;
+  out->n_pinned = p->p.n_pinned;
+  out->n_disk = p->p.n_disk;
+}
+ss_status ss_plan_to_json(const ss_plan* p, char** out_json, size_t* out_len) {
+  std::string s;
+  const ss_status st = guard([&] {
+    need(p != nullptr, "ss_plan_to_json: null plan");
+    s = tsb::json_write(tsb::plan_to_json(p->desc->d, p->p));
+  });
+  return st != SS_OK ? st : give_text(s, out_json, out_len);
+}
+
+// ---- context ----
+void ss_options_defaults_sized(ss_options* o, uint32_t size) { sized_defaults(o, size, options_defaults); }
+
+ss_status ss_open(const ss_desc* d, const ss_budget* budget, const ss_plan* plan, const ss_options* opt, ss_ctx** out) {
+  return guard([&] {
+    need(d && budget && out, "ss_open: null argument");
+    need(!plan || plan->desc == d, "ss_open: plan was made from another descriptor");
+    ss_options o = versioned(opt, options_defaults, "ss_open options");
+    for (uint32_t* r : {&o.reserved0, &o.reserved1, &o.reserved2, &o.reserved3, &o.reserved4, &o.reserved5,
+                        &o.reserved6, &o.reserved7, &o.reserved8, &o.reserved9, &o.reserved10, &o.reserved11,
+                        &o.reserved12, &o.reserved13})
+      *r = 0;
+    tsb::require(o.backend == SS_BACKEND_CUDA, SS_E_UNSUPPORTED,
+                 "ss_open: this build has only the CUDA backend (ss_options.backend = SS_BACKEND_CUDA); the CPU and "
+                 "HIP backends are not built");
+    need(!o.weight_dirs || !o.weight_dirs[0], "ss_open: weight_dirs (multi-location files) is not in this build");
+    need(!o.budget, "ss_open: whole-device budget ledgers are not in this build");
+    need(!o.source_identity_n, "ss_open: source identities are not in this build");
+    ss_budget bb = versioned(budget, budget_defaults, "ss_open budget");
+    bb.reserved0 = 0;
+    need(!plan || tsb::same_budget(plan->p.budget, bb), "ss_open: the plan was made with another budget");
+    const tsb::Plan p = plan ? plan->p : tsb::plan_make(d->d, bb, {});
+    need(o.forward_mode == SS_FORWARD_HOST || o.forward_mode == SS_FORWARD_DEVICE_GATED, "ss_open: unknown forward_mode");
+    if (o.forward_mode == SS_FORWARD_DEVICE_GATED) {
+      auto dg = tsb::open_dg_context(d->d, p, o);
+      *out = new ss_ctx{nullptr, std::move(dg)};
+    } else {
+      need(o.policy == SS_POLICY_LRU, "ss_open: host mode supports SS_POLICY_LRU in this build");
+      auto h = tsb::open_host_context(d->d, bb, p, o);
+      *out = new ss_ctx{std::move(h), nullptr};
+    }
+  });
+}
+void ss_close(ss_ctx* c) { delete c; }
+int ss_source_direct(const ss_ctx* c, int source) {
+  if (!c) return -1;
+  if (c->dg) return source < 0 || source >= c->dg->n_sources() ? -1 : c->dg->source_direct(source) ? 1 : 0;
+  return source < 0 || source >= c->host->n_sources() ? -1 : c->host->source_direct(source) ? 1 : 0;
+}
+
+ss_status ss_seed(ss_ctx* c, int layer, const int32_t* units, int n) {
+  return ctx_guard(c, [&] {
+    if (c->dg) c->dg->seed(layer, units, n);
+    else c->host->seed(layer, units, n);
+  });
+}
+ss_status ss_begin(ss_ctx* c, const uint32_t* rows, int n_layers) {
+  return ctx_guard(c, [&] {
+    if (c->dg) c->dg->begin(rows, n_layers);
+    else c->host->begin(rows, n_layers);
+  });
+}
+ss_status ss_layer_routes(ss_ctx* c, int layer, const int32_t* ids, int n) {
+  return ctx_guard(c, [&] { host_of(c, "ss_layer_routes").routes(layer, ids, n); });
+}
+ss_status ss_layer_routes_dev(ss_ctx* c, int layer, const int32_t* ids_dev, int n, void* s) {
+  return ctx_guard(c, [&] { host_of(c, "ss_layer_routes_dev").routes_dev(layer, ids_dev, n, s); });
+}
+ss_status ss_layer_all(ss_ctx* c, int layer) {
+  return ctx_guard(c, [&] { host_of(c, "ss_layer_all").routes_all(layer); });
+}
+ss_status ss_prefetch(ss_ctx*, int, const int32_t*, int, ss_prefetch_kind) { return unsupported("ss_prefetch"); }
+ss_status ss_prefetch_layer(ss_ctx*, int) { return unsupported("ss_prefetch_layer"); }
+ss_status ss_host_prefetch(ss_ctx*, int, const int32_t*, int) { return unsupported("ss_host_prefetch"); }
+ss_status ss_host_prefetch_layer(ss_ctx*, int) { return unsupported("ss_host_prefetch_layer"); }
+ss_status ss_acquire(ss_ctx* c, int layer, void* s, ss_layer_view* out) {
+  return ctx_guard(c, [&] {
+    need(out != nullptr, "ss_acquire: null view");
+    host_of(c, "ss_acquire").acquire(layer, s, true, out);
+  });
+}
+ss_status ss_acquire_groups(ss_ctx* c, int layer, void* s, ss_layer_view* out) {
+  return ctx_guard(c, [&] {
+    need(out != nullptr, "ss_acquire_groups: null view");
+    host_of(c, "ss_acquire_groups").acquire(layer, s, false, out);
+  });
+}
+ss_status ss_group_wait(ss_ctx* c, int layer, int group, void* s) {
+  return ctx_guard(c, [&] { host_of(c, "ss_group_wait").group_wait(layer, group, s); });
+}
+ss_status ss_release(ss_ctx* c, int layer, void* s) {
+  return ctx_guard(c, [&] { host_of(c, "ss_release").release(layer, s); });
+}
+ss_status ss_end(ss_ctx* c) {
+  return ctx_guard(c, [&] {
+    if (c->dg) c->dg->end();
+    else c->host->end();
+  });
+}
+ss_status ss_check_unit(ss_ctx* c, int layer, int unit) {
+  return ctx_guard(c, [&] {
+    if (c->dg) c->dg->check_unit(layer, unit);
+    else c->host->check_unit(layer, unit);
+  });
+}
+
+ss_status ss_lookahead_select(const float* scores, int rows, int n_experts, int top_k, int32_t* out, int max_out,
+                              int* n_out) {
+  return guard([&] {
+    need(scores && out && n_out && rows >= 0 && n_experts > 0 && top_k > 0 && top_k <= n_experts && max_out >= 0,
+         "ss_lookahead_select: bad argument");
+    // per row its top_k by (score desc, id asc); the union ordered by (best rank, best score, id)
+    std::vector<int> rank(size_t(n_experts), top_k);
+    std::vector<float> best(size_t(n_experts), 0.0f);
+    std::vector<int> idx(static_cast<size_t>(n_experts), 0);
+    for (int r = 0; r < rows; ++r) {
+      const float* s = scores + size_t(r) * size_t(n_experts);
+      for (int e = 0; e < n_experts; ++e) idx[size_t(e)] = e;
+      std::partial_sort(idx.begin(), idx.begin() + top_k, idx.end(),
+                        [&](int a, int b) { return s[a] != s[b] ? s[a] > s[b] : a < b; });
+      for (int k = 0; k < top_k; ++k) {
+        const int e = idx[size_t(k)];
+        if (k < rank[size_t(e)] || (k == rank[size_t(e)] && s[e] > best[size_t(e)])) {
+          rank[size_t(e)] = k;
+          best[size_t(e)] = s[e];
+        }
+      }
+    }
+    std::vector<int> u;
+    for (int e = 0; e < n_experts; ++e)
+      if (rank[size_t(e)] < top_k) u.push_back(e);
+    std::sort(u.begin(), u.end(), [&](int a, int b) {
+      if (rank[size_t(a)] != rank[size_t(b)]) return rank[size_t(a)] < rank[size_t(b)];
+      if (best[size_t(a)] != best[size_t(b)]) return best[size_t(a)] > best[size_t(b)];
+      return a < b;
+    });
+    const int n = std::min(int(u.size()), max_out);
+    for (int i = 0; i < n; ++i) out[i] = u[size_t(i)];
+    *n_out = n;
+  });
+}
+
+// ---- stats ----
+ss_status ss_stats_layer(const ss_ctx* c, int layer, ss_layer_stats* out) {
+  return guard([&] {
+    need(c && out, "ss_stats_layer: bad argument");
+    if (c->dg) c->dg->layer_stats(layer, out);
+    else c->host->layer_stats(layer, out);
+  });
+}
+ss_status ss_stats_total(const ss_ctx* c, ss_layer_stats* out) {
+  return guard([&] {
+    need(c && out, "ss_stats_total: bad argument");
+    if (c->dg) c->dg->total_stats(out);
+    else c->host->total_stats(out);
+  });
+}
+void ss_stats_reset(ss_ctx* c) {
+  if (!c) return;
+  (void)guard([&] {
+    if (c->dg) c->dg->reset_stats();
+    else c->host->reset_stats();
+  });
+}
+void ss_set_stats_hook(ss_ctx* c, ss_stats_hook hook, void* user) {
+  if (c && c->host) c->host->set_hook(hook, user);
+}
+ss_status ss_stats_to_json(const ss_ctx* c, char** out_json, size_t* out_len) {
+  std::string s;
+  const ss_status st = guard([&] {
+    need(c != nullptr, "ss_stats_to_json: null context");
+    s = c->dg ? c->dg->stats_json() : c->host->stats_json();
+  });
+  return st != SS_OK ? st : give_text(s, out_json, out_len);
+}
+ss_status ss_stats_exclusive_sized(const ss_ctx* c, ss_exclusive_stats* out, uint32_t size) {
+  return guard([&] {
+    need(c && out && size >= 4, "ss_stats_exclusive: bad argument");
+    ss_exclusive_stats s{};
+    if (c->dg) c->dg->exclusive_stats(&s);
+    else c->host->exclusive_stats(&s);
+    give_sized(out, size, s);
+  });
+}
+ss_status ss_stats_snapshot_sized(const ss_ctx*, ss_layer_stats*, ss_snapshot_info*, uint32_t) {
+  return unsupported("ss_stats_snapshot");
+}
+ss_status ss_stats_snapshot_json(const ss_ctx*, char**, size_t*) { return unsupported("ss_stats_snapshot_json"); }
+
+// ---- device-gated ----
+ss_status ss_dg_get_device_view_sized(const ss_ctx* c, ss_dg_device_view* out, uint32_t size) {
+  return guard([&] {
+    need(c && out && size >= 4, "ss_dg_get_device_view: bad argument");
+    ss_dg_device_view v;
+    dg_of(c, "ss_dg_get_device_view").device_view(&v);
+    const size_t n = size < sizeof v ? size : sizeof v;
+    std::memcpy(out, &v, n);
+    out->struct_size = uint32_t(n);
+  });
+}
+int ss_dg_gated_index(const ss_ctx* c, int layer) { return c && c->dg ? c->dg->gated_index(layer) : -1; }
+ss_status ss_dg_enqueue_begin(ss_ctx* c, void* stream) {
+  return ctx_guard(c, [&] { dg_of(c, "ss_dg_enqueue_begin").enqueue_begin(stream); });
+}
+ss_status ss_dg_enqueue_export(ss_ctx* c, int g, const int32_t* ids_dev, int n, int n_pred, void* stream) {
+  return ctx_guard(c, [&] { dg_of(c, "ss_dg_enqueue_export").enqueue_export(g, ids_dev, n, n_pred, stream); });
+}
+ss_status ss_dg_enqueue_predict(ss_ctx* c, int g, const int32_t* ids_dev, int n, void* stream) {
+  return ctx_guard(c, [&] { dg_of(c, "ss_dg_enqueue_predict").enqueue_predict(g, ids_dev, n, stream); });
+}
+ss_status ss_dg_enqueue_wait(ss_ctx* c, int g, void* stream) {
+  return ctx_guard(c, [&] { dg_of(c, "ss_dg_enqueue_wait").enqueue_wait(g, stream); });
+}
+ss_status ss_dg_enqueue_end(ss_ctx* c, void* stream) {
+  return ctx_guard(c, [&] { dg_of(c, "ss_dg_enqueue_end").enqueue_end(stream); });
+}
+ss_status ss_dg_keep(ss_ctx* c, int g, const int32_t* ids, int n) {
+  return ctx_guard(c, [&] { dg_of(c, "ss_dg_keep").keep(g, ids, n); });
+}
+ss_status ss_dg_residency(ss_ctx* c, ss_dg_unit* out, uint32_t cap, uint32_t* total) {
+  return ctx_guard(c, [&] {
+    need((out || !cap) && total, "ss_dg_residency: bad argument");
+    *total = dg_of(c, "ss_dg_residency").residency(out, cap);
+  });
+}
+ss_status ss_dg_set_sched(ss_ctx* c, uint32_t wb_defer, uint32_t flush_ready) {
+  return ctx_guard(c, [&] { dg_of(c, "ss_dg_set_sched").set_sched(wb_defer, flush_ready); });
+}
+ss_status ss_dg_set_budgets(ss_ctx* c, uint32_t spare_target, uint32_t per_layer, uint32_t per_token) {
+  return ctx_guard(c, [&] { dg_of(c, "ss_dg_set_budgets").set_budgets(spare_target, per_layer, per_token); });
+}
+ss_status ss_dg_timeline_sized(const ss_ctx* c, int g, ss_dg_layer_timeline* out, uint32_t size) {
+  return guard([&] {
+    need(c && out && size >= 4, "ss_dg_timeline: bad argument");
+    ss_dg_layer_timeline t;
+    dg_of(c, "ss_dg_timeline").timeline(g, &t);
+    give_sized(out, size, t);
+  });
+}
+ss_status ss_dg_boundary_timeline_sized(const ss_ctx* c, ss_dg_boundary_timeline* out, uint32_t size) {
+  return guard([&] {
+    need(c && out && size >= 4, "ss_dg_boundary_timeline: bad argument");
+    ss_dg_boundary_timeline t;
+    dg_of(c, "ss_dg_boundary_timeline").boundary_timeline(&t);
+    give_sized(out, size, t);
+  });
+}
+ss_status ss_stats_dg_sized(const ss_ctx* c, ss_dg_stats* out, uint32_t size) {
+  return guard([&] {
+    need(c && out && size >= 4, "ss_stats_dg: bad argument");
+    ss_dg_stats s;
+    dg_of(c, "ss_stats_dg").stats(&s);
+    give_sized(out, size, s);
+  });
+}
+ss_status ss_dg_reset_open(ss_ctx* c) {
+  return ctx_guard(c, [&] { dg_of(c, "ss_dg_reset_open").reset_open(); });
+}
+ss_status ss_dg_end_rows(ss_ctx* c, uint32_t rows) {
+  return ctx_guard(c, [&] {
+    need(rows > 0, "ss_dg_end_rows: rows must be positive");
+    dg_of(c, "ss_dg_end_rows").end();
+  });
+}
+ss_status ss_dg_set_policy(ss_ctx* c, ss_policy policy) {
+  return ctx_guard(c, [&] {
+    dg_of(c, "ss_dg_set_policy");
+    tsb::require(policy == SS_POLICY_LRU, SS_E_INVALID, "ss_dg_set_policy: this build has the LRU policy only");
+  });
+}
+
+// ---- test hooks ----
+ss_status ss_test_dg_mutate(ss_ctx* c, int m) { return ctx_guard(c, [&] { dg_of(c, "ss_test_dg_mutate").test_mutate(m); }); }
+ss_status ss_test_dg_pressure(ss_ctx* c, uint32_t f, uint32_t r) {
+  return ctx_guard(c, [&] { dg_of(c, "ss_test_dg_pressure").test_pressure(f, r); });
+}
+ss_status ss_test_dg_check(ss_ctx* c) {
+  if (!c) return SS_E_INVALID;
+  return guard([&] { dg_of(c, "ss_test_dg_check").test_check(); });
+}
+ss_status ss_test_dg_gate(ss_ctx* c, int stream, void* event) {
+  return ctx_guard(c, [&] { dg_of(c, "ss_test_dg_gate").test_gate(stream, event); });
+}
+ss_status ss_test_dg_flags(ss_ctx* c, uint32_t flags) {
+  return ctx_guard(c, [&] { dg_of(c, "ss_test_dg_flags").test_flags(flags); });
+}
+ss_status ss_test_dg_coming(ss_ctx* c, uint32_t* out) {
+  return ctx_guard(c, [&] {
+    need(out != nullptr, "ss_test_dg_coming: null output");
+    *out = dg_of(c, "ss_test_dg_coming").test_coming();
+  });
+}
+ss_status ss_test_dg_stop_service(ss_ctx* c) {
+  return ctx_guard(c, [&] { dg_of(c, "ss_test_dg_stop_service").test_stop_service(); });
+}
+
+ss_status tsb_test_dg_table(ss_ctx* c, int32_t* out, uint32_t cap) {
+  if (!c) return SS_E_INVALID;
+  return guard([&] { dg_of(c, "tsb_test_dg_table").test_table(out, cap); });
+}
+
+// ---- not in this build ----
+void ss_dg_winpf_defaults_sized(ss_dg_winpf_params*, uint32_t) {}
+ss_status ss_dg_winpf_set(ss_ctx*, const ss_dg_winpf_params*) { return unsupported("ss_dg_winpf_set"); }
+ss_status ss_dg_window_hint(ss_ctx*, const int32_t*, const float*, uint32_t) { return unsupported("ss_dg_window_hint"); }
+ss_status ss_recipe_from_text(const char*, size_t, const char*, ss_recipe**) { return unsupported("ss_recipe_from_text"); }
+ss_status ss_recipe_from_file(const char*, ss_recipe**) { return unsupported("ss_recipe_from_file"); }
+void ss_recipe_free(ss_recipe*) {}
+ss_status ss_recipe_add_profile(ss_recipe*, const char*, size_t, const char*, const char*, size_t) {
+  return unsupported("ss_recipe_add_profile");
+}
+ss_status ss_recipe_add_overrides(ss_recipe*, const char*, size_t, const char*) {
+  return unsupported("ss_recipe_add_overrides");
+}
+ss_status ss_recipe_set(ss_recipe*, const char*, const char*, const char*) { return unsupported("ss_recipe_set"); }
+ss_status ss_recipe_to_json(const ss_recipe*, char**, size_t*) { return unsupported("ss_recipe_to_json"); }
+ss_status ss_recipe_explain(const ss_recipe*, char**, size_t*) { return unsupported("ss_recipe_explain"); }
+ss_status ss_recipe_match(const ss_recipe*, const char*, size_t, char**, size_t*) { return unsupported("ss_recipe_match"); }
+ss_status ss_recipe_select(const ss_recipe*, const char*, size_t, char**, size_t*) {
+  return unsupported("ss_recipe_select");
+}
+ss_status ss_recipe_plan(const ss_recipe*, const char*, const char*, int, const char*, const ss_desc*, const double*,
+                         size_t, const ss_desc* const*, const double* const*, const size_t*, size_t, ss_budget*,
+                         ss_options*, ss_plan**, char**, size_t*) {
+  return unsupported("ss_recipe_plan");
+}
+void ss_mfile_options_defaults_sized(ss_mfile_options*, uint32_t) {}
+ss_status ss_mfile_open(const char*, const char*, const ss_mfile_options*, ss_mfile**) { return unsupported("ss_mfile_open"); }
+void ss_mfile_close(ss_mfile*) {}
+uint64_t ss_mfile_size(const ss_mfile*) { return 0; }
+uint32_t ss_mfile_alignment(const ss_mfile*) { return 0; }
+int ss_mfile_multi(const ss_mfile*) { return 0; }
+ss_status ss_mfile_pread(ss_mfile*, void*, uint64_t, uint64_t, uint64_t*) { return unsupported("ss_mfile_pread"); }
+ss_status ss_mfile_preadv(ss_mfile*, const ss_mfile_io*, uint32_t) { return unsupported("ss_mfile_preadv"); }
+ss_status ss_mfile_get_counters(const ss_mfile*, ss_mfile_counters*) { return unsupported("ss_mfile_get_counters"); }
+const char* ss_mfile_location_path(const ss_mfile*, int) { return nullptr; }
+const char* ss_mfile_open_report(const ss_mfile*) { return nullptr; }
+ss_status ss_mfile_location_info(const ss_mfile*, uint32_t, ss_mfile_location*) {
+  return unsupported("ss_mfile_location_info");
+}
+void ss_budget_in_defaults_sized(ss_budget_in*, uint32_t) {}
+ss_status ss_budget_plan(const ss_budget_in*, ss_budget_out*) { return unsupported("ss_budget_plan"); }
+size_t ss_budget_plan_json(const ss_budget_in*, const ss_budget_out*, char*, size_t) { return 0; }
+ss_status ss_budget_ledger_create(uint64_t, uint64_t, ss_budget_ledger**) { return unsupported("ss_budget_ledger_create"); }
+void ss_budget_ledger_free(ss_budget_ledger*) {}
+ss_status ss_budget_ledger_add(ss_budget_ledger*, ss_budget_kind, const char*, uint64_t) {
+  return unsupported("ss_budget_ledger_add");
+}
+ss_status ss_budget_ledger_sub(ss_budget_ledger*, ss_budget_kind, const char*, uint64_t) {
+  return unsupported("ss_budget_ledger_sub");
+}
+ss_status ss_budget_ledger_observe_device(ss_budget_ledger*, uint64_t) {
+  return unsupported("ss_budget_ledger_observe_device");
+}
+ss_status ss_budget_ledger_stats(const ss_budget_ledger*, ss_budget_stats*) { return unsupported("ss_budget_ledger_stats"); }
+ss_status ss_budget_ledger_observe(ss_budget_ledger*, const char*, uint64_t, uint64_t) {
+  return unsupported("ss_budget_ledger_observe");
+}
+int ss_budget_ledger_within_caps(const ss_budget_ledger*) { return 0; }
+ss_status ss_budget_in_dg_library(ss_budget_in*, const ss_desc*, const ss_options*) {
+  return unsupported("ss_budget_in_dg_library");
+}
+ss_status ss_dg_make_resident(ss_ctx*, int, const int32_t*, int) { return unsupported("ss_dg_make_resident"); }
+void ss_dg_round_defaults_sized(ss_dg_round_params*, uint32_t) {}
+ss_status ss_dg_round_sized(ss_ctx*, const ss_dg_round_params*, ss_dg_round_result*, uint32_t) {
+  return unsupported("ss_dg_round");
+}
+ss_status ss_dg_round_cancel(ss_ctx*) { return unsupported("ss_dg_round_cancel"); }
+ss_status ss_dg_round_seed_counts(ss_ctx*, const ss_dg_unit*, const float*, uint32_t) {
+  return unsupported("ss_dg_round_seed_counts");
+}
+void ss_devprof_detect_opts_defaults_sized(ss_devprof_detect_opts*, uint32_t) {}
+ss_status ss_devprof_detect(const ss_devprof_detect_opts*, ss_devprof**) { return unsupported("ss_devprof_detect"); }
+ss_status ss_devprof_from_json(const char*, size_t, ss_devprof**) { return unsupported("ss_devprof_from_json"); }
+ss_status ss_devprof_merge_json(ss_devprof*, const char*, size_t, const char*) { return unsupported("ss_devprof_merge_json"); }
+void ss_devprof_free(ss_devprof*) {}
+ss_status ss_devprof_to_json(const ss_devprof*, char**, size_t*) { return unsupported("ss_devprof_to_json"); }
+ss_status ss_devprof_hash(const ss_devprof*, char[17]) { return unsupported("ss_devprof_hash"); }
+ss_status ss_devprof_probe_report(const ss_devprof*, const char*, char**, size_t*) {
+  return unsupported("ss_devprof_probe_report");
+}
+ss_status ss_devprof_get(const ss_devprof*, ss_devprof_info*) { return unsupported("ss_devprof_get"); }
+ss_status ss_devprof_limit(const ss_devprof*, const char*, uint64_t*) { return unsupported("ss_devprof_limit"); }
+ss_status ss_devprof_get_device(const ss_devprof*, uint32_t, ss_devprof_device*) { return unsupported("ss_devprof_get_device"); }
+ss_status ss_devprof_budget(const ss_devprof*, uint32_t, ss_budget_in*) { return unsupported("ss_devprof_budget"); }
+void ss_devprof_topology_in_defaults_sized(ss_devprof_topology_in*, uint32_t) {}
+ss_status ss_devprof_topology(const ss_devprof* const*, uint32_t, const ss_devprof_topology_in*, ss_devprof_topology_out*) {
+  return unsupported("ss_devprof_topology");
+}
+void ss_devprof_piece_in_defaults_sized(ss_devprof_piece_in*, uint32_t) {}
+ss_status ss_devprof_piece_rows(const ss_devprof*, const ss_devprof_piece_in*, uint32_t*) {
+  return unsupported("ss_devprof_piece_rows");
+}
+void ss_pack_options_defaults_sized(ss_pack_options*, uint32_t) {}
+ss_status ss_pack_open(const char*, const ss_pack_options*, ss_pack**) { return unsupported("ss_pack_open"); }
+void ss_pack_close(ss_pack*) {}
+uint64_t ss_pack_records(const ss_pack*) { return 0; }
+ss_status ss_pack_entry_at_sized(const ss_pack*, uint64_t, ss_pack_entry*, uint32_t) { return unsupported("ss_pack_entry_at"); }
+ss_status ss_pack_find_sized(const ss_pack*, int, int, const char*, ss_pack_entry*, uint32_t) {
+  return unsupported("ss_pack_find");
+}
+ss_status ss_pack_segment_at(const ss_pack*, uint64_t, uint32_t, ss_pack_segment*) { return unsupported("ss_pack_segment_at"); }
+ss_status ss_pack_unit_find(const ss_pack*, int, int, ss_pack_unit*) { return unsupported("ss_pack_unit_find"); }
+ss_status ss_pack_read(ss_pack*, uint64_t, uint32_t, uint32_t, void*) { return unsupported("ss_pack_read"); }
+ss_status ss_pack_readv(ss_pack*, const ss_pack_read_req*, uint32_t) { return unsupported("ss_pack_readv"); }
+ss_status ss_pack_read_unit(ss_pack*, int, int, void*) { return unsupported("ss_pack_read_unit"); }
+ss_status ss_pack_dg_descriptor(ss_pack*, const char*, size_t, char**, size_t*) { return unsupported("ss_pack_dg_descriptor"); }
+uint32_t ss_pack_files(const ss_pack*) { return 0; }
+int ss_pack_has_layout(const ss_pack*, const char*) { return 0; }
+ss_status ss_pack_file_identity(const ss_pack*, uint32_t, ss_file_identity*) { return unsupported("ss_pack_file_identity"); }
+ss_status ss_pack_info_json(const ss_pack*, char**, size_t*) { return unsupported("ss_pack_info_json"); }
+ss_status ss_pack_verify_full(ss_pack*, char**, size_t*) { return unsupported("ss_pack_verify_full"); }
+ss_status ss_pack_writer_begin(const char*, const char*, size_t, ss_pack_writer**) { return unsupported("ss_pack_writer_begin"); }
+ss_status ss_pack_writer_record_begin(ss_pack_writer*, const ss_pack_record_spec*) {
+  return unsupported("ss_pack_writer_record_begin");
+}
+ss_status ss_pack_writer_record_write(ss_pack_writer*, const void*, uint64_t) {
+  return unsupported("ss_pack_writer_record_write");
+}
+ss_status ss_pack_writer_record_end(ss_pack_writer*) { return unsupported("ss_pack_writer_record_end"); }
+ss_status ss_pack_writer_add(ss_pack_writer*, const ss_pack_record_spec*, const void*) { return unsupported("ss_pack_writer_add"); }
+ss_status ss_pack_writer_finish(ss_pack_writer*, char*) { return unsupported("ss_pack_writer_finish"); }
+void ss_pack_writer_abort(ss_pack_writer*) {}
+ss_status ss_dg_set_clean_evict(ss_ctx*, uint32_t) { return unsupported("ss_dg_set_clean_evict"); }
+ss_status ss_dg_begin_layer(ss_ctx*, int, int) { return unsupported("ss_dg_begin_layer"); }
+ss_status ss_dg_enqueue_export_part(ss_ctx*, int, int, const int32_t*, int, void*) {
+  return unsupported("ss_dg_enqueue_export_part");
+}
+ss_status ss_dg_enqueue_wait_part(ss_ctx*, int, int, void*) { return unsupported("ss_dg_enqueue_wait_part"); }
+ss_status ss_dg_enqueue_end_layer(ss_ctx*, void*) { return unsupported("ss_dg_enqueue_end_layer"); }
+ss_status ss_dg_set_pf_revert_unused(ss_ctx*, uint32_t) { return unsupported("ss_dg_set_pf_revert_unused"); }
+
+}  // extern "C"

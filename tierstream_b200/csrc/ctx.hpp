@@ -1,0 +1,87 @@
+// The two context kinds behind ss_ctx: host forward mode (host_ctx.cpp) and device-gated decode (dg_ctx.cu). capi.cpp
+// dispatches the ss_* calls to them and maps their exceptions to ss_status.
+#pragma once
+
+#include <cstdint>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "desc.hpp"
+#include "plan.hpp"
+#include "strix_stream/ss.h"
+
+namespace tsb {
+
+class DgContext {
+ public:
+  virtual ~DgContext() = default;
+  virtual bool poisoned() const = 0;
+  virtual void poison() = 0;
+  virtual int n_sources() const = 0;
+  virtual bool source_direct(int i) const = 0;
+  virtual int gated_index(int layer) const = 0;
+  virtual void begin(const uint32_t* rows, int n_layers) = 0;
+  virtual void end() = 0;
+  virtual void seed(int layer, const int32_t* units, int n) = 0;
+  virtual void check_unit(int layer, int unit) = 0;
+  virtual void device_view(ss_dg_device_view* v) const = 0;
+  virtual void enqueue_begin(void* s) = 0;
+  virtual void enqueue_export(int g, const int32_t* ids, int n, int n_pred, void* s) = 0;
+  virtual void enqueue_predict(int g, const int32_t* ids, int n, void* s) = 0;
+  virtual void enqueue_wait(int g, void* s) = 0;
+  virtual void enqueue_end(void* s) = 0;
+  virtual void keep(int g, const int32_t* ids, int n) = 0;
+  virtual uint32_t residency(ss_dg_unit* out, uint32_t cap) = 0;
+  virtual void set_sched(uint32_t wb_defer, uint32_t flush_ready) = 0;
+  virtual void set_budgets(uint32_t spare_target, uint32_t per_layer, uint32_t per_token) = 0;
+  virtual void timeline(int g, ss_dg_layer_timeline* out) const = 0;
+  virtual void boundary_timeline(ss_dg_boundary_timeline* out) const = 0;
+  virtual void stats(ss_dg_stats* out) const = 0;
+  virtual void layer_stats(int layer, ss_layer_stats* out) const = 0;
+  virtual void total_stats(ss_layer_stats* out) const = 0;
+  virtual void reset_stats() = 0;
+  virtual void exclusive_stats(ss_exclusive_stats* out) const = 0;
+  virtual std::string stats_json() const = 0;
+  virtual void reset_open() = 0;
+  // test hooks (ss_test.h), refused unless opened with dg_test_hooks
+  virtual void test_mutate(int m) = 0;
+  virtual void test_pressure(uint32_t free_per_token, uint32_t evict_recent) = 0;
+  virtual void test_check() = 0;
+  virtual void test_gate(int stream, void* event) = 0;
+  virtual void test_flags(uint32_t flags) = 0;
+  virtual uint32_t test_coming() = 0;
+  virtual void test_stop_service() = 0;
+  virtual uint32_t test_table(int32_t* out, uint32_t cap) = 0;  // the device's slot table; returns the key count
+};
+
+std::unique_ptr<DgContext> open_dg_context(const Desc& d, const Plan& p, const ss_options& o);
+
+class HostContext {
+ public:
+  virtual ~HostContext() = default;
+  virtual bool poisoned() const = 0;
+  virtual void poison() = 0;
+  virtual int n_sources() const = 0;
+  virtual bool source_direct(int i) const = 0;
+  virtual void seed(int layer, const int32_t* units, int n) = 0;
+  virtual void begin(const uint32_t* rows, int n_layers) = 0;
+  virtual void routes(int layer, const int32_t* ids, int n) = 0;
+  virtual void routes_dev(int layer, const int32_t* ids_dev, int n, void* stream) = 0;
+  virtual void routes_all(int layer) = 0;
+  virtual void acquire(int layer, void* stream, bool wait_all, ss_layer_view* out) = 0;
+  virtual void group_wait(int layer, int group, void* stream) = 0;
+  virtual void release(int layer, void* stream) = 0;
+  virtual void end() = 0;
+  virtual void check_unit(int layer, int unit) = 0;
+  virtual void layer_stats(int layer, ss_layer_stats* out) const = 0;
+  virtual void total_stats(ss_layer_stats* out) const = 0;
+  virtual void reset_stats() = 0;
+  virtual void set_hook(ss_stats_hook hook, void* user) = 0;
+  virtual void exclusive_stats(ss_exclusive_stats* out) const = 0;
+  virtual std::string stats_json() const = 0;
+};
+
+std::unique_ptr<HostContext> open_host_context(const Desc& d, const ss_budget& b, const Plan& p, const ss_options& o);
+
+}  // namespace tsb

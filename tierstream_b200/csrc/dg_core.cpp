@@ -1,0 +1,845 @@
+#include "dg_core.hpp"
+
+#include <algorithm>
+#include <chrono>
+
+#include "errors.hpp"
+
+namespace tsb {
+
+SlotCache::SlotCache(const CacheConfig& cfg, Mover* m) : c_(cfg), m_(m) {
+  base_.assign(1, 0);
+  for (uint32_t n : c_.n_units) {
+    require(n >= 1, SS_E_INVALID, "device-gated: a gated layer without units");
+    base_.push_back(base_.back() + n);
+  }
+  keys_ = base_.back();
+  require(c_.persistent_slots >= 1 && c_.spare_target <= c_.persistent_slots, SS_E_INVALID,
+          "device-gated: spare target above the persistent slots");
+  const uint64_t slots = uint64_t(c_.persistent_slots) + 2ull * c_.bank_slots;
+  require(slots < 0x7fffffffull, SS_E_INVALID, "device-gated: more than 2^31 - 1 slots");
+  slots_ = uint32_t(slots);
+  bank_first_ = c_.persistent_slots;
+  e_.assign(keys_, Entry{});
+  table_.assign(keys_, -1);
+  bank_key_.assign(2u * size_t(c_.bank_slots), kNil);
+  pf_layer_.assign(gated(), 0);
+  layer_missed_.assign(gated(), 0);
+  lc_.assign(gated(), LayerCounts{});
+  if (c_.prefetch_reserve_auto) c_.prefetch_reserve = std::min<uint32_t>(24, c_.spare_target / 4);
+  require(m_->parts() >= 1, SS_E_INVALID, "device-gated: a unit without parts");
+  for (uint32_t p = 0; p < m_->parts(); ++p) unit_bytes_ += m_->part_bytes(p);
+  apply_wb_defer();
+  victims_.reserve(c_.persistent_slots);
+}
+
+SlotCache::~SlotCache() {
+  for (void* ev : all_events_) m_->event_destroy(ev);
+}
+
+[[noreturn]] void SlotCache::broken(const std::string& what) const {
+  fail(SS_E_BACKEND, "device-gated: cache invariant broken: " + what);
+}
+
+uint32_t SlotCache::gated_of(uint32_t k) const {
+  return uint32_t(std::upper_bound(base_.begin(), base_.end(), k) - base_.begin()) - 1;
+}
+
+uint32_t SlotCache::coming() const {
+  uint32_t n = 0;
+  for (uint32_t k : coming_) n += e_[k].home == Home::Coming ? 1u : 0u;
+  return n;
+}
+
+void SlotCache::apply_wb_defer() {
+  if (c_.wb_defer) {
+    wb_stream_ = c_.wb_on_d2h ? Mover::kD2h : Mover::kDem;
+    layer_bytes_ = c_.wb_layer_bytes ? c_.wb_layer_bytes : m_->part_bytes(0);
+    max_outstanding_ = c_.wb_max_outstanding ? c_.wb_max_outstanding : 2 * unit_bytes_;
+    require(layer_bytes_ <= uint64_t(INT64_MAX) / 4, SS_E_INVALID, "device-gated: dg_wb_layer_bytes too large");
+    if (c_.wb_on_d2h && !post_ready_ev_) post_ready_ev_ = event();
+  } else {
+    wb_stream_ = Mover::kDem;
+    layer_bytes_ = 0;
+    max_outstanding_ = 0;
+  }
+}
+
+void SlotCache::place(const std::vector<uint32_t>& order) {
+  const uint32_t dev_max = c_.persistent_slots - c_.spare_target;
+  std::vector<uint8_t> taken(keys_, 0);
+  std::vector<uint32_t> dev;
+  for (uint32_t k : order) {
+    require(k < keys_, SS_E_INVALID, "device-gated: resident key out of range");
+    if (!taken[k] && dev.size() < dev_max) {
+      taken[k] = 1;
+      dev.push_back(k);
+    }
+  }
+  require(uint64_t(keys_) - dev.size() <= c_.blocks, SS_E_CAPACITY,
+          "device-gated: fewer host blocks than non-resident units");
+  int32_t next_block = 0;
+  for (uint32_t k = 0; k < keys_; ++k) {
+    e_[k] = Entry{};
+    if (!taken[k]) e_[k].block = next_block++;  // Host home, blocks in key order
+    table_[k] = -1;
+  }
+  head_ = tail_ = kNil;
+  for (uint32_t i = 0; i < dev.size(); ++i) {
+    Entry& x = e_[dev[i]];
+    x.home = Home::Device;
+    x.slot = int32_t(i);
+    table_[dev[i]] = x.slot;
+  }
+  for (size_t i = dev.size(); i-- > 0;) push_front(dev[i]);  // dev[0] ends up most recent
+  on_device_ = uint32_t(dev.size());
+  free_slots_.clear();
+  free_blocks_.clear();
+  for (uint32_t s = c_.persistent_slots; s-- > on_device_;) free_slots_.push_back(int32_t(s));
+  for (int32_t b = int32_t(c_.blocks); b-- > next_block;) free_blocks_.push_back(b);
+  open_c_ = c_;
+  open_e_ = e_;
+  open_table_ = table_;
+  open_free_slots_ = free_slots_;
+  open_free_blocks_ = free_blocks_;
+  open_head_ = head_;
+  open_tail_ = tail_;
+  open_on_device_ = on_device_;
+}
+
+// ---- the recency list (head = most recently used) ----
+void SlotCache::unlink(uint32_t k) {
+  Entry& x = e_[k];
+  if (!x.listed) return;
+  if (x.prev != kNil) e_[x.prev].next = x.next;
+  else head_ = x.next;
+  if (x.next != kNil) e_[x.next].prev = x.prev;
+  else tail_ = x.prev;
+  x.prev = x.next = kNil;
+  x.listed = false;
+}
+
+void SlotCache::push_front(uint32_t k) {
+  Entry& x = e_[k];
+  x.prev = kNil;
+  x.next = head_;
+  if (head_ != kNil) e_[head_].prev = k;
+  else tail_ = k;
+  head_ = k;
+  x.listed = true;
+}
+
+void* SlotCache::event() {
+  if (!pool_.empty()) {
+    void* ev = pool_.back();
+    pool_.pop_back();
+    return ev;
+  }
+  void* ev = m_->event_create();
+  all_events_.push_back(ev);
+  return ev;
+}
+
+void SlotCache::publish(Mover::Stream s, uint32_t k, int32_t v) {
+  table_[k] = v;
+  m_->publish(s, k, v);
+}
+
+void SlotCache::to_host(uint32_t k) {
+  Entry& x = e_[k];
+  if (x.block < 0) broken("a unit without a block left the device without a write-back");
+  x.slot = -1;
+  x.home = Home::Host;
+}
+
+// Finished write-backs in submission order: the unit's home becomes its block and its slot is free; a discarded one
+// (the unit was resurrected) only returns its block.
+uint32_t SlotCache::collect() {
+  uint32_t n = 0;
+  while (!wbs_.empty()) {
+    Writeback& w = wbs_.front();
+    if (!m_->done(w.done)) break;
+    Entry& x = e_[w.key];
+    x.wb_pending = false;
+    if (w.discard) {
+      free_blocks_.push_back(w.block);
+    } else {
+      x.home = Home::Host;
+      x.block = w.block;
+      x.slot = -1;
+      free_slots_.push_back(w.slot);
+    }
+    ++n;
+    outstanding_ -= w.bytes;
+    st_.wb_completed_bytes += w.bytes;
+    pool_.push_back(w.done);
+    wbs_.pop_front();
+  }
+  st_.writebacks_done += n;
+  return n;
+}
+
+void SlotCache::submit_part(Deferred& d) {
+  const uint32_t p = d.parts_done;
+  m_->d2h(wb_stream_, d.slot, d.block, int32_t(p));
+  ++d.parts_done;
+  const uint64_t b = m_->part_bytes(p);
+  d.bytes += b;
+  outstanding_ += b;
+  st_.wb_issued_bytes += b;
+}
+
+void* SlotCache::record_front(bool discard) {
+  Deferred& d = deferred_.front();
+  void* ev = event();
+  m_->record(ev, wb_stream_);
+  wbs_.push_back({d.key, d.slot, d.block, ev, discard, d.bytes});
+  deferred_.pop_front();
+  return ev;
+}
+
+void* SlotCache::finish_front() {
+  Deferred& d = deferred_.front();
+  while (d.parts_done < m_->parts()) submit_part(d);
+  return record_front(false);
+}
+
+void SlotCache::issue_writebacks(uint32_t g, const std::function<bool()>& ahead) {
+  if (deferred_.empty()) {
+    credit_ = 0;
+    return;
+  }
+  if (g + 1 >= gated()) return;  // never behind the last layer: the boundary's sync would wait for it
+  const int64_t grant = int64_t(layer_bytes_);
+  credit_ = std::min(credit_ + grant, grant);  // a debt carries over, unused credit does not
+  st_.collected_mid += collect();
+  bool behind_ready = false;
+  while (credit_ > 0 && !deferred_.empty() && outstanding_ < max_outstanding_ && !(ahead && ahead())) {
+    if (wb_stream_ == Mover::kD2h && !behind_ready) {
+      m_->record(post_ready_ev_, Mover::kDem);
+      m_->wait(Mover::kD2h, post_ready_ev_);
+      behind_ready = true;
+    }
+    Deferred& d = deferred_.front();
+    credit_ -= int64_t(m_->part_bytes(d.parts_done));
+    if (d.parts_done + 1 == m_->parts()) finish_front();
+    else submit_part(d);
+  }
+}
+
+// A demand with no free slot while write-backs are deferred: wait for the oldest live write-back in flight (or finish
+// the deferred front and wait for it) until a slot is free.
+void SlotCache::force_free_slot() {
+  while (free_slots_.empty() && !deferred_.empty()) {
+    void* ev = nullptr;
+    for (const Writeback& w : wbs_)
+      if (!w.discard) {
+        ev = w.done;
+        break;
+      }
+    if (!ev) ev = finish_front();
+    ++st_.wb_forced;
+    const auto t0 = std::chrono::steady_clock::now();
+    m_->event_sync(ev);
+    st_.wb_forced_wait_ns += uint64_t(
+        std::chrono::duration_cast<std::chrono::nanoseconds>(std::chrono::steady_clock::now() - t0).count());
+    st_.collected_mid += collect();
+  }
+}
+
+// Bank g & 1 of the demand bank slots; a bank is reused two gated layers later, when the device has finished the
+// layer that used it before. The slot's previous unit goes back to its block and its entry is withdrawn first.
+int32_t SlotCache::bank_slot(uint32_t g) {
+  const uint32_t b = g & 1u;
+  if (bank_seq_[b] != seq_ || bank_layer_[b] != g) {
+    bank_seq_[b] = seq_;
+    bank_layer_[b] = g;
+    bank_next_[b] = 0;
+  }
+  if (bank_next_[b] >= c_.bank_slots) return -1;
+  const uint32_t idx = b * c_.bank_slots + bank_next_[b]++;
+  const int32_t slot = int32_t(bank_first_ + idx);
+  const uint32_t old = bank_key_[idx];
+  if (old != kNil && e_[old].home == Home::Bank && e_[old].slot == slot) {
+    to_host(old);
+    publish(Mover::kDem, old, -1);
+  }
+  bank_key_[idx] = kNil;
+  return slot;
+}
+
+void SlotCache::begin_token(uint32_t seq) {
+  seq_ = seq;
+  pf_token_ = 0;
+  demand_free_used_ = 0;
+  std::fill(pf_layer_.begin(), pf_layer_.end(), 0u);
+  std::fill(layer_missed_.begin(), layer_missed_.end(), uint8_t(0));
+  pred_.clear();
+  pred_layer_ = kNil;
+}
+
+bool SlotCache::fetch(uint32_t g, uint32_t unit, bool prefetch) {
+  const uint32_t k = key(g, unit);
+  Entry& x = e_[k];
+  if (prefetch && (pf_layer_[g] >= c_.prefetch_per_layer || pf_token_ >= c_.prefetch_per_token)) return false;
+  switch (x.home) {
+    case Home::Coming:
+    case Home::Device:
+    case Home::Bank:
+      return false;
+    case Home::Evicting: {  // resurrection: the slot still holds the bytes (a write-back only reads them)
+      for (auto it = deferred_.begin(); it != deferred_.end(); ++it) {
+        if (it->key != k) continue;
+        if (it->parts_done == 0) {  // nothing submitted: cancelled, its block free again
+          free_blocks_.push_back(it->block);
+          deferred_.erase(it);
+          x.wb_pending = false;
+          ++st_.wb_cancelled;
+          st_.wb_cancelled_bytes += unit_bytes_;
+        } else {  // partly submitted (only the front can be): recorded as a discard
+          if (it != deferred_.begin()) broken("parts submitted behind the deferred front");
+          st_.wb_cancelled_bytes += unit_bytes_ - it->bytes;
+          record_front(true);
+        }
+        x.home = Home::Device;
+        x.block = -1;
+        publish(Mover::kDem, k, x.slot);
+        push_front(k);
+        ++on_device_;
+        ++st_.resurrected;
+        return true;
+      }
+      for (Writeback& w : wbs_)
+        if (w.key == k && !w.discard) {
+          w.discard = true;
+          break;
+        }
+      x.home = Home::Device;
+      x.block = -1;
+      publish(Mover::kDem, k, x.slot);
+      push_front(k);
+      ++on_device_;
+      ++st_.resurrected;
+      return true;
+    }
+    case Home::Host:
+      break;
+  }
+  const size_t reserve = prefetch ? c_.prefetch_reserve : 0u;
+  if (free_slots_.size() <= reserve || (pressure_ && !prefetch)) st_.collected_mid += collect();
+  const bool capped = !prefetch && pressure_ && demand_free_used_ >= pressure_free_;
+  if (!prefetch && !capped && free_slots_.empty()) force_free_slot();
+  int32_t slot = -1;
+  bool bank = false;
+  if (!capped && free_slots_.size() > reserve) {
+    if (!prefetch) ++demand_free_used_;
+    slot = free_slots_.back();
+    free_slots_.pop_back();
+  } else if (prefetch) {
+    return false;
+  } else {
+    slot = bank_slot(g);
+    if (slot >= 0) {
+      bank = true;
+    } else {  // more distinct misses than a bank holds: only an internal error gets here
+      force_free_slot();
+      while (free_slots_.empty() && !wbs_.empty()) {
+        m_->event_sync(wbs_.front().done);
+        collect();
+        ++st_.stalled;
+      }
+      if (free_slots_.empty()) fail(SS_E_BACKEND, "device-gated: no free slot, no bank slot, no write-back to wait for");
+      slot = free_slots_.back();
+      free_slots_.pop_back();
+    }
+  }
+  const Mover::Stream s = prefetch ? Mover::kPf : Mover::kDem;
+  if (mut_ == kEntryBeforeCopy) {  // test-only fault: the entry before its bytes
+    publish(s, k, slot);
+    m_->h2d(s, slot, x.block);
+  } else {
+    m_->h2d(s, slot, x.block);
+    publish(s, k, slot);
+  }
+  x.slot = slot;
+  x.via_pf = prefetch;
+  x.used = false;
+  if (prefetch) {
+    x.pf_done = event();
+    m_->record(x.pf_done, s);
+  }
+  if (bank) {
+    x.home = Home::Bank;
+    bank_key_[size_t(slot) - bank_first_] = k;
+    banked_.push_back(k);
+    ++st_.bank_serves;
+    ++lc_[g].bank_serves;
+  } else {
+    x.home = Home::Coming;
+    coming_.push_back(k);
+    push_front(k);
+    ++on_device_;
+  }
+  if (prefetch) {
+    ++st_.prefetched;
+    ++lc_[g].prefetched;
+    ++pf_layer_[g];
+    ++pf_token_;
+  } else {
+    ++st_.fetched;
+    ++lc_[g].fetched;
+  }
+  return true;
+}
+
+void SlotCache::cover(uint32_t g, uint32_t unit) {
+  Entry& x = e_[key(g, unit)];
+  if (x.home == Home::Coming && x.via_pf && x.pf_done && mut_ != kNoCover) {
+    m_->wait(Mover::kDem, x.pf_done);
+    ++st_.covered_waits;
+  }
+}
+
+void SlotCache::use(uint32_t g, uint32_t unit, bool was_miss) {
+  const uint32_t k = key(g, unit);
+  Entry& x = e_[k];
+  ++st_.lookups;
+  ++lc_[g].lookups;
+  if (was_miss) {
+    ++st_.misses;
+    ++lc_[g].misses;
+    if (!layer_missed_[g]) {
+      layer_missed_[g] = 1;
+      ++st_.miss_layers;
+    }
+  }
+  if (x.via_pf && !x.used) {
+    x.used = true;
+    ++st_.prefetch_used;
+    ++lc_[g].prefetch_used;
+  }
+  if (x.listed) {
+    unlink(k);
+    push_front(k);
+  }
+}
+
+void SlotCache::serve_demand(uint32_t g, const uint32_t* ids, uint32_t n, uint64_t mask) {
+  const uint32_t nu = units(g);
+  for (uint32_t i = 0; i < n; ++i)
+    require(ids[i] < nu, SS_E_INVALID,
+            "device-gated: layer " + std::to_string(g) + " exported id " + std::to_string(ids[i]) + " of " +
+                std::to_string(nu));
+  // masked occurrences in export order: a repeated id is fetched at its first occurrence, covered at the others
+  for (uint32_t i = 0; i < n; ++i) {
+    if (!(mask >> i & 1u)) continue;
+    const Home h = e_[key(g, ids[i])].home;
+    if (h == Home::Device || h == Home::Coming || h == Home::Bank) {
+      cover(g, ids[i]);
+      ++st_.covered;
+    } else {
+      fetch(g, ids[i], false);
+    }
+  }
+  if (mask) m_->ready(g, seq_);
+}
+
+void SlotCache::serve_use(uint32_t g, const uint32_t* ids, uint32_t n, uint64_t mask) {
+  const bool have_pred = pred_layer_ == g;
+  uniq_.assign(ids, ids + n);
+  std::sort(uniq_.begin(), uniq_.end());
+  uniq_.erase(std::unique(uniq_.begin(), uniq_.end()), uniq_.end());
+  for (uint32_t id : uniq_) {
+    bool miss = false;
+    for (uint32_t i = 0; i < n; ++i)
+      if (ids[i] == id && (mask >> i & 1u)) miss = true;
+    use(g, id, miss);
+    if (have_pred && std::find(pred_.begin(), pred_.end(), id) != pred_.end()) ++st_.predicted_true;
+  }
+  pred_.clear();
+  pred_layer_ = kNil;
+}
+
+// The prediction for layer g_next: deduplicated in order, invalid ids dropped; each one a budgeted prefetch. The
+// device running ahead does not skip it (the reference's default prediction admission).
+void SlotCache::serve_prediction(uint32_t g_next, const uint32_t* pred, uint32_t n, bool ahead) {
+  (void)ahead;
+  if (g_next >= gated()) return;
+  const uint32_t nu = units(g_next);
+  uniq_.clear();
+  for (uint32_t i = 0; i < n; ++i) {
+    if (pred[i] >= nu) {
+      ++st_.pred_invalid;
+      continue;
+    }
+    if (std::find(uniq_.begin(), uniq_.end(), pred[i]) == uniq_.end()) uniq_.push_back(pred[i]);
+  }
+  st_.predicted += uniq_.size();
+  pred_.assign(uniq_.begin(), uniq_.end());
+  pred_layer_ = g_next;
+  for (uint32_t id : pred_) fetch(g_next, id, true);
+}
+
+void SlotCache::end_token(const std::vector<uint32_t>& keep) {
+  m_->sync(Mover::kDem);
+  m_->sync(Mover::kPf);
+  std::vector<uint8_t> kept;
+  if (!keep.empty()) {
+    kept.assign(keys_, 0);
+    for (uint32_t k : keep)
+      if (k < keys_) kept[k] = 1;
+  }
+  for (uint32_t k : coming_) {  // arrivals become device homes; their source blocks are free
+    Entry& x = e_[k];
+    if (x.home != Home::Coming) continue;
+    x.home = Home::Device;
+    x.via_pf = false;
+    if (x.pf_done) {
+      pool_.push_back(x.pf_done);
+      x.pf_done = nullptr;
+    }
+    if (x.block >= 0) {
+      free_blocks_.push_back(x.block);
+      x.block = -1;
+    }
+  }
+  coming_.clear();
+  for (uint32_t k : banked_) {  // bank units go back to their blocks
+    Entry& x = e_[k];
+    if (x.home == Home::Bank) {
+      to_host(k);
+      table_[k] = -1;
+    }
+    if (x.pf_done) {
+      pool_.push_back(x.pf_done);
+      x.pf_done = nullptr;
+    }
+    x.via_pf = false;
+  }
+  banked_.clear();
+  std::fill(bank_key_.begin(), bank_key_.end(), kNil);
+  bank_seq_[0] = bank_seq_[1] = 0;
+  bank_layer_[0] = bank_layer_[1] = kNil;
+  collect();
+  size_t pending = deferred_.size();
+  for (const Writeback& w : wbs_) pending += w.discard ? 0u : 1u;
+  const size_t base = free_slots_.size() + pending;
+  victims_.clear();
+  size_t got = 0;
+  bool short_blocks = false;
+  auto eligible = [&](uint32_t k) {
+    const Entry& x = e_[k];
+    return x.home == Home::Device && !x.wb_pending && !(kept.size() && kept[k]);
+  };
+  auto accept = [&](uint32_t k) {
+    Entry& x = e_[k];
+    if (free_blocks_.empty()) {
+      ++st_.evict_short;
+      short_blocks = true;
+      return false;
+    }
+    const int32_t b = free_blocks_.back();
+    free_blocks_.pop_back();
+    unlink(k);
+    --on_device_;
+    x.home = Home::Evicting;
+    x.block = b;
+    x.wb_pending = true;
+    table_[k] = -1;
+    victims_.push_back(k);
+    ++got;
+    return true;
+  };
+  for (uint32_t k = tail_; k != kNil && base + got < c_.spare_target;) {
+    const uint32_t prev = e_[k].prev;
+    if (eligible(k) && !accept(k)) break;
+    k = prev;
+  }
+  if (pressure_ && pressure_recent_ && !short_blocks) {  // test pressure: the most recent ones too
+    uint32_t n = 0;
+    for (uint32_t k = head_; k != kNil && n < pressure_recent_;) {
+      const uint32_t next = e_[k].next;
+      if (eligible(k)) {
+        if (!accept(k)) break;
+        ++n;
+      }
+      k = next;
+    }
+  }
+  const size_t n_evict = victims_.size();
+  m_->upload_table(table_.data(), keys_);  // the table first, then the write-backs behind it
+  const size_t n_old = deferred_.size(), carry = std::max(n_evict, prev_evict_);
+  const size_t n_flush = n_old > carry ? n_old - carry : 0;
+  prev_evict_ = n_evict;
+  credit_ = 0;
+  for (size_t i = 0; c_.wb_defer && i < n_evict; ++i) {
+    const uint32_t k = victims_[i];
+    deferred_.push_back({k, e_[k].slot, e_[k].block, 0, 0});
+    ++st_.wb_deferred;
+    ++st_.evicted;
+    ++lc_[gated_of(k)].evicted;
+  }
+  const uint64_t issued0 = st_.wb_issued_bytes;
+  for (size_t i = 0; i < n_flush; ++i) finish_front();
+  st_.wb_boundary_flushed += n_flush;
+  st_.wb_boundary_flushed_bytes += st_.wb_issued_bytes - issued0;
+  for (size_t i = 0; !c_.wb_defer && i < n_evict; ++i) {
+    const uint32_t k = victims_[i];
+    const Entry& x = e_[k];
+    m_->d2h(Mover::kD2h, x.slot, x.block, -1);
+    void* ev = event();
+    m_->record(ev, Mover::kD2h);
+    wbs_.push_back({k, x.slot, x.block, ev, false, unit_bytes_});
+    outstanding_ += unit_bytes_;
+    st_.wb_issued_bytes += unit_bytes_;
+    ++st_.evicted;
+    ++lc_[gated_of(k)].evicted;
+  }
+  ++st_.tokens;
+}
+
+uint32_t SlotCache::seed(const std::vector<uint32_t>& keys) {
+  if (!coming_.empty()) m_->sync(Mover::kPf);
+  collect();
+  uint32_t n = 0;
+  for (uint32_t k : keys) {
+    require(k < keys_, SS_E_INVALID, "ss_seed: unit out of range");
+    Entry& x = e_[k];
+    if (x.home != Home::Host || free_slots_.size() <= c_.spare_target) continue;
+    const int32_t slot = free_slots_.back();
+    free_slots_.pop_back();
+    m_->h2d(Mover::kDem, slot, x.block);
+    free_blocks_.push_back(x.block);
+    x.block = -1;
+    x.slot = slot;
+    x.home = Home::Device;
+    table_[k] = slot;
+    push_front(k);
+    ++on_device_;
+    ++n;
+  }
+  if (n) m_->upload_table(table_.data(), keys_);  // syncs kDem: the copies landed before their blocks are reused
+  return n;
+}
+
+void SlotCache::drain() {
+  while (!deferred_.empty()) finish_front();
+  m_->sync(Mover::kDem);
+  m_->sync(Mover::kPf);
+  m_->sync(Mover::kD2h);
+}
+
+std::vector<uint32_t> SlotCache::residency() const {
+  std::vector<uint32_t> out;
+  out.reserve(on_device_);
+  for (uint32_t k = head_; k != kNil; k = e_[k].next)
+    if (e_[k].home == Home::Device) out.push_back(k);
+  return out;
+}
+
+void SlotCache::set_wb_defer(bool on) {
+  if (on == c_.wb_defer) return;
+  if (!on)
+    while (!deferred_.empty()) finish_front();
+  c_.wb_defer = on;
+  apply_wb_defer();
+  credit_ = 0;
+  prev_evict_ = 0;
+}
+
+void SlotCache::set_spare_target(uint32_t n) {
+  require(n <= c_.persistent_slots, SS_E_INVALID, "device-gated: spare target above the persistent slots");
+  c_.spare_target = n;
+  if (c_.prefetch_reserve_auto) c_.prefetch_reserve = std::min<uint32_t>(24, n / 4);
+}
+
+void SlotCache::set_prefetch_budget(uint32_t per_layer, uint32_t per_token) {
+  c_.prefetch_per_layer = per_layer;
+  c_.prefetch_per_token = per_token;
+}
+
+void SlotCache::set_pressure(uint32_t free_per_token, uint32_t evict_recent) {
+  pressure_ = free_per_token != 0 || evict_recent != 0;
+  pressure_free_ = free_per_token;
+  pressure_recent_ = evict_recent;
+}
+
+// Locations: slots [0, P), blocks [P, P + blocks), and the reset staging buffer. Every misplaced unit moves once:
+// chains that end in a free location first (each move fills the hole the previous one left), then the remaining
+// cycles through the staging buffer. The mover executes each move before the next one reads its destination.
+void SlotCache::reset_open() {
+  require(open_e_.size() == keys_, SS_E_INVALID, "device-gated: reset before place");
+  drain();
+  for (const Writeback& w : wbs_) m_->event_sync(w.done);
+  collect();
+  if (!wbs_.empty()) broken("reset could not collect every write-back");
+  for (Entry& x : e_)
+    if (x.pf_done) {
+      m_->event_sync(x.pf_done);
+      pool_.push_back(x.pf_done);
+      x.pf_done = nullptr;
+    }
+  const size_t P = c_.persistent_slots, N = P + c_.blocks, stage = N;
+  std::vector<size_t> cur(keys_), dst(keys_);
+  std::vector<uint32_t> occupant(N + 1, kNil), wanted(N + 1, kNil);
+  for (uint32_t k = 0; k < keys_; ++k) {
+    const Entry& x = e_[k];
+    if (x.home == Home::Evicting) broken("reset left an evicting unit");
+    const bool on_slot = x.home == Home::Device || (x.home == Home::Coming && x.block < 0);
+    cur[k] = on_slot ? size_t(x.slot) : P + size_t(x.block);
+    const Entry& o = open_e_[k];
+    dst[k] = o.home == Home::Device ? size_t(o.slot) : P + size_t(o.block);
+    occupant[cur[k]] = k;
+    wanted[dst[k]] = k;
+  }
+  // plan every move first (bookkeeping only), then execute them in order; consecutive slot-to-slot moves share
+  // launches: a move's wave is one after every earlier move that reads its destination or writes its source
+  struct Move {
+    size_t from, to;
+  };
+  std::vector<Move> plan;
+  auto move = [&](uint32_t k, size_t to) {
+    const size_t from = cur[k];
+    if (to > N || occupant[to] != kNil) broken("reset would overwrite a live source");
+    plan.push_back({from, to});
+    occupant[from] = kNil;
+    occupant[to] = k;
+    cur[k] = to;
+  };
+  for (size_t loc = 0; loc < N; ++loc) {
+    size_t hole = loc;
+    while (hole < N && occupant[hole] == kNil && wanted[hole] != kNil) {
+      const uint32_t k = wanted[hole];
+      const size_t next = cur[k];
+      move(k, hole);
+      hole = next;
+    }
+  }
+  for (uint32_t k = 0; k < keys_; ++k) {
+    if (cur[k] == dst[k]) continue;
+    size_t hole = cur[k];
+    move(k, stage);
+    while (hole != dst[k]) {
+      const uint32_t next = wanted[hole];
+      if (next == kNil) broken("reset cycle without a predecessor");
+      const size_t from = cur[next];
+      move(next, hole);
+      hole = from;
+    }
+    move(k, hole);
+  }
+  auto blk = [&](size_t loc) { return loc == stage ? -1 : int32_t(loc - P); };
+  std::vector<std::pair<int32_t, int32_t>> d2d;
+  std::vector<uint32_t> wave;
+  auto flush_d2d = [&] {
+    if (d2d.empty()) return;
+    m_->d2d_moves(d2d, wave);
+    d2d.clear();
+    wave.clear();
+  };
+  for (const Move& mv : plan) {
+    ++st_.reset_moves;
+    st_.reset_bytes += unit_bytes_;
+    if (mv.from < P && mv.to < P) {
+      uint32_t w = 0;
+      for (size_t i = 0; i < d2d.size(); ++i)
+        if (size_t(d2d[i].first) == mv.to || size_t(d2d[i].second) == mv.from) w = std::max(w, wave[i] + 1);
+      d2d.push_back({int32_t(mv.from), int32_t(mv.to)});
+      wave.push_back(w);
+      continue;
+    }
+    flush_d2d();
+    if (mv.from < P) {
+      m_->d2h(Mover::kD2h, int32_t(mv.from), blk(mv.to), -1);
+      m_->sync(Mover::kD2h);
+    } else if (mv.to < P) {
+      m_->h2d(Mover::kDem, int32_t(mv.to), blk(mv.from));
+      m_->sync(Mover::kDem);
+    } else {
+      m_->h2h(blk(mv.from), blk(mv.to));
+    }
+  }
+  flush_d2d();
+  c_ = open_c_;
+  apply_wb_defer();
+  std::copy(open_e_.begin(), open_e_.end(), e_.begin());
+  std::copy(open_table_.begin(), open_table_.end(), table_.begin());
+  free_slots_ = open_free_slots_;
+  free_blocks_ = open_free_blocks_;
+  head_ = open_head_;
+  tail_ = open_tail_;
+  on_device_ = open_on_device_;
+  coming_.clear();
+  banked_.clear();
+  std::fill(bank_key_.begin(), bank_key_.end(), kNil);
+  bank_seq_[0] = bank_seq_[1] = 0;
+  bank_layer_[0] = bank_layer_[1] = kNil;
+  bank_next_[0] = bank_next_[1] = 0;
+  std::fill(pf_layer_.begin(), pf_layer_.end(), 0u);
+  pf_token_ = 0;
+  pred_.clear();
+  pred_layer_ = kNil;
+  std::fill(layer_missed_.begin(), layer_missed_.end(), uint8_t(0));
+  pressure_ = false;
+  pressure_free_ = pressure_recent_ = demand_free_used_ = 0;
+  prev_evict_ = 0;
+  credit_ = 0;
+  outstanding_ = 0;
+  m_->upload_table(table_.data(), keys_);
+}
+
+void SlotCache::check() const {
+  std::vector<uint8_t> slot_used(slots_, 0), block_used(c_.blocks, 0);
+  auto take = [&](std::vector<uint8_t>& v, int64_t i, const char* what) {
+    if (i < 0 || size_t(i) >= v.size() || v[size_t(i)]) broken(what);
+    v[size_t(i)] = 1;
+  };
+  uint32_t listed = 0, dev = 0;
+  for (uint32_t k = head_; k != kNil; k = e_[k].next) {
+    if (++listed > keys_) broken("the recency list has a cycle");
+    const Home h = e_[k].home;
+    if (h != Home::Device && h != Home::Coming) broken("a listed unit is not on the device");
+  }
+  for (uint32_t k = 0; k < keys_; ++k) {
+    const Entry& x = e_[k];
+    switch (x.home) {
+      case Home::Host:
+        take(block_used, x.block, "a host unit without its own block");
+        if (table_[k] != -1) broken("a host unit with a published entry");
+        if (x.listed) broken("a host unit in the recency list");
+        break;
+      case Home::Device:
+      case Home::Coming:
+        ++dev;
+        take(slot_used, x.slot, "a device unit without its own slot");
+        if (x.slot >= int32_t(c_.persistent_slots)) broken("a device unit in a bank slot");
+        if (table_[k] != x.slot) broken("a device unit's entry is not its slot");
+        if (!x.listed) broken("a device unit outside the recency list");
+        if (x.home == Home::Coming) take(block_used, x.block, "a coming unit without its source block");
+        else if (x.block >= 0) broken("a device unit still holding a block");
+        break;
+      case Home::Bank:
+        take(slot_used, x.slot, "a bank unit without its own slot");
+        take(block_used, x.block, "a bank unit without its block");
+        if (x.slot < int32_t(c_.persistent_slots)) broken("a bank unit in a persistent slot");
+        if (table_[k] != x.slot) broken("a bank unit's entry is not its slot");
+        break;
+      case Home::Evicting:
+        take(slot_used, x.slot, "an evicting unit without its slot");
+        take(block_used, x.block, "an evicting unit without its destination block");
+        if (table_[k] != -1) broken("an evicting unit with a published entry");
+        break;
+    }
+  }
+  if (dev != on_device_ || dev != listed) broken("the device count disagrees with the homes");
+  for (int32_t s : free_slots_) take(slot_used, s, "a free slot that is also in use");
+  for (int32_t b : free_blocks_) take(block_used, b, "a free block that is also in use");
+  for (const Writeback& w : wbs_)
+    if (w.discard) take(block_used, w.block, "a discarded write-back block in use");
+  for (uint32_t s = 0; s < c_.persistent_slots; ++s)
+    if (!slot_used[s]) broken("a persistent slot neither free nor held");
+  for (uint32_t b = 0; b < c_.blocks; ++b)
+    if (!block_used[b]) broken("a block neither free nor held");
+}
+
+}  // namespace tsb

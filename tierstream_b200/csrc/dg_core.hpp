@@ -1,0 +1,219 @@
+// Device-gated decode: the slot cache's state machine, with no device API in it. A Mover performs the copies, the
+// table publications and the events on three streams; the CUDA mover lives in dg_ctx.cu (copy engines or this
+// library's gather kernels), a host mover in dg_host_mover.cpp (the CPU tests and the deterministic replay).
+//
+// Every gated unit (key = unit_base[g] + unit) has one home: a slot of the arena shared by all gated layers
+// (Device; Coming while its copy is in flight; Bank for a demand served through a per-layer bank slot; Evicting while
+// its write-back runs) or a pinned block (Host). Inside a token entries only go from -1 to a slot, published on the
+// stream that copied the bytes; evictions happen at the boundary (end_token), whose write-backs are either enqueued
+// there or deferred part by part into the next token's served layers.
+//
+// The decisions are those of the reference's DgCore (dg_core.cpp) for its two-tier LRU configuration, so the slot
+// table after every token matches it on the same trace when the schedule is deterministic:
+//   - open placement: residents by priority into slots 0.., every other key a block in key order
+//     (dg_core.cpp:769-858); free slots and blocks are LIFO stacks whose next is the lowest index;
+//   - a demand miss takes the last free slot, else (write-backs deferred) waits for one, else its layer's bank slot
+//     (bank g & 1, reused two layers later) (dg_core.cpp:1146-1368, 1059-1097);
+//   - a prefetch keeps prefetch_reserve slots free and stays under the per-layer and per-token budgets;
+//   - the boundary admits the token's arrivals, returns bank units to their blocks, collects finished write-backs,
+//     then evicts from the recency tail until free + pending write-backs reaches the spare target, one free block per
+//     victim (dg_core.cpp:1636-1927); deferred write-backs are carried and flushed by the same counts.
+#pragma once
+
+#include <cstdint>
+#include <deque>
+#include <functional>
+#include <string>
+#include <utility>
+#include <vector>
+
+namespace tsb {
+
+class Mover {
+ public:
+  enum Stream { kDem = 0, kPf = 1, kD2h = 2 };
+  virtual ~Mover() = default;
+  virtual uint32_t parts() const = 0;
+  virtual uint64_t part_bytes(uint32_t p) const = 0;
+  // Every part of `block` into `slot` (block -1 = the one-unit reset staging buffer).
+  virtual void h2d(Stream s, int32_t slot, int32_t block) = 0;
+  // Part p (p < 0: every part) of `slot` into `block`.
+  virtual void d2h(Stream s, int32_t slot, int32_t block, int32_t p) = 0;
+  // Reset: slot-to-slot moves (src, dst). Moves of one wave touch disjoint slots and run together; waves run in
+  // ascending order. Complete when the call returns.
+  virtual void d2d_moves(const std::vector<std::pair<int32_t, int32_t>>& moves, const std::vector<uint32_t>& wave) = 0;
+  virtual void h2h(int32_t src_block, int32_t dst_block) = 0;
+  // slot_of[key] = v after everything enqueued on s so far (a release at system scope).
+  virtual void publish(Stream s, uint32_t key, int32_t v) = 0;
+  // ready[g] = seq on kDem after everything enqueued there.
+  virtual void ready(uint32_t g, uint32_t seq) = 0;
+  virtual void* event_create() = 0;
+  virtual void event_destroy(void* ev) = 0;
+  virtual void record(void* ev, Stream s) = 0;
+  virtual void wait(Stream s, void* ev) = 0;  // device side
+  virtual bool done(void* ev) = 0;            // host query
+  virtual void event_sync(void* ev) = 0;
+  virtual void sync(Stream s) = 0;
+  virtual void upload_table(const int32_t* table, uint32_t n) = 0;  // the whole table on kDem, then sync
+};
+
+struct CacheConfig {
+  std::vector<uint32_t> n_units;  // per gated layer
+  uint32_t persistent_slots = 0;  // residents + spare slots: [0, persistent_slots)
+  uint32_t bank_slots = 0;        // per bank: [persistent_slots, persistent_slots + 2 * bank_slots)
+  uint32_t blocks = 0;
+  uint32_t spare_target = 0;
+  uint32_t prefetch_reserve = 0;
+  bool prefetch_reserve_auto = false;  // follows the spare target: min(24, spare_target / 4)
+  uint32_t prefetch_per_layer = 4, prefetch_per_token = 48;
+  bool wb_defer = false, wb_on_d2h = false;
+  uint64_t wb_layer_bytes = 0, wb_max_outstanding = 0;
+};
+
+struct CacheStats {
+  uint64_t tokens = 0, lookups = 0, misses = 0, covered = 0, fetched = 0, prefetched = 0, prefetch_used = 0;
+  uint64_t resurrected = 0, bank_serves = 0, collected_mid = 0, evicted = 0, evict_short = 0, writebacks_done = 0;
+  uint64_t stalled = 0, pred_invalid = 0, covered_waits = 0, predicted = 0, predicted_true = 0, miss_layers = 0;
+  uint64_t wb_deferred = 0, wb_cancelled = 0, wb_forced = 0, wb_boundary_flushed = 0;
+  uint64_t wb_issued_bytes = 0, wb_completed_bytes = 0, wb_cancelled_bytes = 0, wb_boundary_flushed_bytes = 0;
+  uint64_t wb_forced_wait_ns = 0;
+  uint64_t reset_moves = 0, reset_bytes = 0;
+};
+
+struct LayerCounts {
+  uint64_t lookups = 0, misses = 0, fetched = 0, bank_serves = 0, prefetched = 0, prefetch_used = 0, evicted = 0;
+};
+
+class SlotCache {
+ public:
+  enum class Home : uint8_t { Host, Device, Coming, Bank, Evicting };
+  enum Mutation { kNone0 = 0, kEntryBeforeCopy = 1, kNoCover = 2 };
+
+  SlotCache(const CacheConfig& cfg, Mover* m);
+  ~SlotCache();
+  SlotCache(const SlotCache&) = delete;
+  SlotCache& operator=(const SlotCache&) = delete;
+
+  // Open: `order` names keys by priority (duplicates ignored); the first persistent_slots - spare_target distinct
+  // ones take slots 0.., in that recency order; every other key takes a block, numbered in key order.
+  void place(const std::vector<uint32_t>& order);
+
+  uint32_t keys() const { return keys_; }
+  uint32_t gated() const { return uint32_t(base_.size() - 1); }
+  uint32_t key(uint32_t g, uint32_t u) const { return base_[g] + u; }
+  uint32_t units(uint32_t g) const { return base_[g + 1] - base_[g]; }
+  uint32_t gated_of(uint32_t k) const;
+  const std::vector<uint32_t>& unit_base() const { return base_; }
+  const std::vector<int32_t>& table() const { return table_; }
+  int32_t slot_of(uint32_t k) const { return e_[k].slot; }
+  int32_t block_of(uint32_t k) const { return e_[k].block; }
+  Home home(uint32_t k) const { return e_[k].home; }
+  uint32_t on_device() const { return on_device_; }
+  uint32_t free_slots() const { return uint32_t(free_slots_.size()); }
+  uint32_t free_blocks() const { return uint32_t(free_blocks_.size()); }
+  uint32_t deferred() const { return uint32_t(deferred_.size()); }
+  uint64_t wb_outstanding_bytes() const { return outstanding_; }
+  const CacheStats& stats() const { return st_; }
+  const std::vector<LayerCounts>& layer_counts() const { return lc_; }
+  const CacheConfig& config() const { return c_; }
+  uint32_t coming() const;
+  // Most recently used first, device homes only.
+  std::vector<uint32_t> residency() const;
+
+  // ---- inside a token (the service thread) ----
+  void begin_token(uint32_t seq);
+  void serve_demand(uint32_t g, const uint32_t* ids, uint32_t n, uint64_t mask);
+  void serve_use(uint32_t g, const uint32_t* ids, uint32_t n, uint64_t mask);
+  void serve_prediction(uint32_t g_next, const uint32_t* pred, uint32_t n, bool ahead);
+  // Deferred write-back parts after layer g was served (its ready already enqueued); ahead() is asked before every
+  // part: a later layer already exported, so no more parts now.
+  void issue_writebacks(uint32_t g, const std::function<bool()>& ahead);
+
+  // ---- between tokens (the engine thread) ----
+  void end_token(const std::vector<uint32_t>& keep);
+  uint32_t seed(const std::vector<uint32_t>& keys);
+  void drain();
+  // Restores the open placement, moving only misplaced units; `plan` receives the slot-to-slot moves in execution
+  // order when given (the mover performs them as they come).
+  void reset_open();
+  void set_wb_defer(bool on);
+  void set_spare_target(uint32_t n);
+  void set_prefetch_budget(uint32_t per_layer, uint32_t per_token);
+  void set_pressure(uint32_t free_per_token, uint32_t evict_recent);
+  void set_mutation(int m) { mut_ = m; }
+  // Every ownership rule (throws SS_E_BACKEND naming the first broken one).
+  void check() const;
+
+ private:
+  static constexpr uint32_t kNil = 0xffffffffu;
+  struct Entry {
+    Home home = Home::Host;
+    int32_t slot = -1, block = -1;
+    uint32_t prev = kNil, next = kNil;
+    bool listed = false, wb_pending = false, via_pf = false, used = false;
+    void* pf_done = nullptr;
+  };
+  struct Writeback {
+    uint32_t key;
+    int32_t slot, block;
+    void* done;
+    bool discard;
+    uint64_t bytes;
+  };
+  struct Deferred {
+    uint32_t key;
+    int32_t slot, block;
+    uint32_t parts_done;
+    uint64_t bytes;
+  };
+
+  void unlink(uint32_t k);
+  void push_front(uint32_t k);
+  void* event();
+  uint32_t collect();
+  void submit_part(Deferred& d);
+  void* record_front(bool discard);
+  void* finish_front();
+  void force_free_slot();
+  int32_t bank_slot(uint32_t g);
+  void to_host(uint32_t k);
+  void publish(Mover::Stream s, uint32_t k, int32_t v);
+  bool fetch(uint32_t g, uint32_t unit, bool prefetch);
+  void cover(uint32_t g, uint32_t unit);
+  void use(uint32_t g, uint32_t unit, bool was_miss);
+  void apply_wb_defer();
+  [[noreturn]] void broken(const std::string& what) const;
+
+  CacheConfig c_, open_c_;
+  Mover* m_;
+  std::vector<uint32_t> base_;
+  uint32_t keys_ = 0, slots_ = 0, bank_first_ = 0;
+  std::vector<Entry> e_, open_e_;
+  std::vector<int32_t> table_, open_table_;
+  std::vector<int32_t> free_slots_, free_blocks_, open_free_slots_, open_free_blocks_;
+  uint32_t head_ = kNil, tail_ = kNil, on_device_ = 0;
+  uint32_t open_head_ = kNil, open_tail_ = kNil, open_on_device_ = 0;
+  std::deque<Writeback> wbs_;
+  std::deque<Deferred> deferred_;
+  Mover::Stream wb_stream_ = Mover::kDem;
+  uint64_t unit_bytes_ = 0, layer_bytes_ = 0, max_outstanding_ = 0, outstanding_ = 0;
+  int64_t credit_ = 0;
+  size_t prev_evict_ = 0;
+  void* post_ready_ev_ = nullptr;
+  std::vector<void*> pool_, all_events_;
+  std::vector<uint32_t> bank_key_;
+  uint32_t bank_seq_[2] = {0, 0}, bank_layer_[2] = {kNil, kNil}, bank_next_[2] = {0, 0};
+  std::vector<uint32_t> pf_layer_;
+  uint32_t pf_token_ = 0;
+  bool pressure_ = false;
+  uint32_t pressure_free_ = 0, pressure_recent_ = 0, demand_free_used_ = 0;
+  std::vector<uint32_t> coming_, banked_, pred_, uniq_, victims_;
+  uint32_t pred_layer_ = kNil;
+  std::vector<uint8_t> layer_missed_;
+  uint32_t seq_ = 0;
+  CacheStats st_;
+  std::vector<LayerCounts> lc_;
+  int mut_ = 0;
+};
+
+}  // namespace tsb

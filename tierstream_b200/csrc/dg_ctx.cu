@@ -1,0 +1,1423 @@
+// Device-gated decode on a B200: the context behind ss_open(forward_mode = SS_FORWARD_DEVICE_GATED).
+//
+// Memory (one context, one device):
+//   HBM    arena: one array per part, `slots` entries of part bytes each (residents, spares, 2 banks, zeroed guard);
+//          slot_of[keys]; control words (seq, abort, errors, any_miss[G], ready[G], unit_base[G + 1], absent_err)
+//          and one completion counter per copy stream for the land kernel.
+//   pinned blocks: P + Q units at a 4 KiB host stride, mapped (the land kernel reads them over PCIe), <= 1 GiB chunks;
+//          one staging unit for reset cycles; a mapped control area with the export records and flags.
+// Per token the engine's graph runs begin / export / wait / end (kernels.cu); a service thread spins on the mapped
+// export flags and drives the slot cache (dg_core.cpp) whose copies, entries and ready words go to the CudaMover: one
+// land-kernel launch per batch (copies, then entries, then ready, published by its last block), or the copy engines
+// plus stream writes when a part is large enough for them to be faster.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <immintrin.h>
+
+#include <algorithm>
+#include <atomic>
+#include <chrono>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <memory>
+#include <mutex>
+#include <thread>
+
+#include "ctx.hpp"
+#include "dg_core.hpp"
+#include "errors.hpp"
+#include "kernels.hpp"
+#include "source_file.hpp"
+#include "xxh64.hpp"
+
+namespace tsb {
+namespace {
+
+using Clock = std::chrono::steady_clock;
+
+void ck(cudaError_t e, const char* what) {
+  if (e != cudaSuccess) {
+    (void)cudaGetLastError();
+    fail(e == cudaErrorMemoryAllocation ? SS_E_NOMEM : SS_E_BACKEND,
+         std::string(what) + ": " + cudaGetErrorString(e));
+  }
+}
+// The few driver functions used here, resolved through the runtime (cudaGetDriverEntryPoint) at the first open: the
+// library links no libcuda, so it loads on a machine without a driver (the CPU tests).
+struct Driver {
+  CUresult (*write_value32)(CUstream, CUdeviceptr, cuuint32_t, unsigned int) = nullptr;
+  CUresult (*error_string)(CUresult, const char**) = nullptr;
+  CUresult (*loading_mode)(CUmoduleLoadingMode*) = nullptr;
+};
+const Driver& driver() {
+  static const Driver d = [] {
+    Driver x;
+    cudaDriverEntryPointQueryResult q{};
+    auto get = [&](const char* name, void** fn) {
+      if (cudaGetDriverEntryPoint(name, fn, cudaEnableDefault, &q) != cudaSuccess || q != cudaDriverEntryPointSuccess)
+        *fn = nullptr;
+    };
+    get("cuStreamWriteValue32", reinterpret_cast<void**>(&x.write_value32));
+    get("cuGetErrorString", reinterpret_cast<void**>(&x.error_string));
+    get("cuModuleGetLoadingMode", reinterpret_cast<void**>(&x.loading_mode));
+    return x;
+  }();
+  return d;
+}
+void ck_drv(CUresult r, const char* what) {
+  if (r != CUDA_SUCCESS) {
+    const char* s = nullptr;
+    if (driver().error_string) driver().error_string(r, &s);
+    fail(SS_E_BACKEND, std::string(what) + ": " + (s ? s : "CUDA driver error"));
+  }
+}
+CUresult write_value32(CUstream s, CUdeviceptr p, cuuint32_t v) {
+  require(driver().write_value32 != nullptr, SS_E_BACKEND, "cuStreamWriteValue32 is not available from the driver");
+  return driver().write_value32(s, p, v, CU_STREAM_WRITE_VALUE_DEFAULT);
+}
+void ck_launch(int e, const char* what) { ck(cudaError_t(e), what); }
+
+inline uint32_t load_acquire(const uint32_t* p) { return __atomic_load_n(p, __ATOMIC_ACQUIRE); }
+inline void store_release(uint32_t* p, uint32_t v) { __atomic_store_n(p, v, __ATOMIC_RELEASE); }
+inline void cpu_relax() { _mm_pause(); }
+
+double us_between(Clock::time_point a, Clock::time_point b) {
+  return std::chrono::duration<double, std::micro>(b - a).count();
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// Layout: what an open needs from the descriptor, the plan and the options, with the reference's refusals
+// (dg_layout.cpp:183-411) for everything this build supports.
+// ---------------------------------------------------------------------------------------------------------------
+struct Layout {
+  std::vector<int> gated;           // descriptor layer of each gated ordinal
+  std::vector<int> ordinal;         // per descriptor layer, -1 when not gated
+  std::vector<uint32_t> unit_base;  // G + 1
+  std::vector<uint64_t> part_bytes, part_offset;
+  uint64_t unit_bytes = 0, host_stride = 0;
+  uint32_t keys = 0, R = 0, D = 0, B = 0, P = 0, Q = 0;
+  uint32_t persistent_slots = 0, slots = 0, guard_slot = 0, blocks = 0;
+  std::vector<uint32_t> residents;  // keys of tier R, key order
+};
+
+Layout make_layout(const Desc& d, const Plan& p, const ss_options& o) {
+  auto refuse = [](ss_status st, const std::string& why) { fail(st, "device-gated: " + why); };
+  const ss_budget& b = p.budget;
+  if (b.tier_mode != SS_TIER_MODE_EXCLUSIVE) refuse(SS_E_INVALID, "needs tier_mode EXCLUSIVE");
+  if (b.pinned_backing) refuse(SS_E_INVALID, "pinned_backing is refused (each unit has one home)");
+  if (o.policy == SS_POLICY_SCORED || o.policy == SS_POLICY_SCORED_AUTO)
+    refuse(SS_E_UNSUPPORTED, "scored eviction is not in this build (use SS_POLICY_LRU)");
+  if (o.policy != SS_POLICY_LRU) refuse(SS_E_INVALID, "policy must be LRU");
+  if (o.pin_planned) refuse(SS_E_INVALID, "needs pin_planned = 0 (planned residents are a warm start)");
+  if (!o.fill_residents) refuse(SS_E_INVALID, "needs fill_residents = 1 (a resident's slot is its only copy)");
+  if (o.readahead_units) refuse(SS_E_INVALID, "readahead_units must be 0 (no gated unit is read from its file)");
+  if (o.spec_persistent) refuse(SS_E_INVALID, "spec_persistent is refused (prediction is the service's)");
+  if (o.dg_max_ids < 1 || o.dg_max_ids > dev::kMaxIds) refuse(SS_E_INVALID, "dg_max_ids must be 1..64 (rows x top_k)");
+  if (o.dg_wait_timeout_ms < 1) refuse(SS_E_INVALID, "dg_wait_timeout_ms must be >= 1");
+  if (o.dg_wb_defer > 1) refuse(SS_E_INVALID, "dg_wb_defer must be 0 or 1");
+  if (o.dg_wb_stream > 1) refuse(SS_E_INVALID, "dg_wb_stream must be 0 or 1");
+  if (o.dg_disk_tier || o.dg_disk_prefetch || o.dg_disk_staging || o.dg_disk_queue || o.dg_inclusive_blocks)
+    refuse(SS_E_UNSUPPORTED, "the three-tier placement (dg_disk_*, dg_inclusive_blocks) is not in this build");
+  if (o.dg_no_admit || o.dg_clean_evict || o.dg_pf_revert_unused || o.dg_pf_strict_admit || o.dg_landing_blocks ||
+      o.dg_bank_keep || o.dg_disk_queue_adapt || o.dg_prior_len || o.dg_score_profile_len)
+    refuse(SS_E_UNSUPPORTED, "an opt-in device-gated policy of the reference that is not in this build is set");
+  Layout x;
+  x.B = o.dg_max_ids;
+  x.ordinal.assign(d.layers.size(), -1);
+  const Layer* shape = nullptr;
+  for (size_t L = 0; L < d.layers.size(); ++L) {
+    const Layer& l = d.layers[L];
+    if (l.n_units == 0) continue;
+    if (!l.streamable)
+      refuse(SS_E_UNSUPPORTED, "layer " + std::to_string(l.index) + " has non-streamable units (every unit is gated)");
+    if (!shape) {
+      shape = &l;
+      if (l.parts.size() > SS_DG_MAX_PARTS)
+        refuse(SS_E_UNSUPPORTED, "more than " + std::to_string(SS_DG_MAX_PARTS) + " parts per unit");
+      uint64_t off = 0;
+      for (const Part& part : l.parts) {
+        if (part.bytes % 256 != 0)
+          refuse(SS_E_UNSUPPORTED, "part " + part.name + " is " + std::to_string(part.bytes) +
+                                       " bytes, not a multiple of 256 (the arena stride equals the part bytes)");
+        x.part_bytes.push_back(part.bytes);
+        x.part_offset.push_back(off);
+        off += part.bytes;
+      }
+      x.unit_bytes = l.unit_bytes;
+    } else {
+      bool same = l.parts.size() == shape->parts.size();
+      for (size_t i = 0; same && i < l.parts.size(); ++i) same = l.parts[i].bytes == shape->parts[i].bytes;
+      if (!same) refuse(SS_E_UNSUPPORTED, "layer " + std::to_string(l.index) + " has another part shape (one arena)");
+    }
+    x.ordinal[L] = int(x.gated.size());
+    x.gated.push_back(int(L));
+  }
+  if (x.gated.empty()) refuse(SS_E_INVALID, "the descriptor has no streamable units");
+  const uint32_t G = uint32_t(x.gated.size());
+  x.host_stride = host_stride(x.unit_bytes);
+  x.unit_base.assign(1, 0);
+  uint64_t keys = 0;
+  for (uint32_t g = 0; g < G; ++g) {
+    const Layer& l = d.layers[size_t(x.gated[g])];
+    uint32_t planned = 0;
+    for (int u = 0; u < l.n_units; ++u) {
+      const uint8_t t = p.tier[size_t(d.unit_base[size_t(x.gated[g])] + u)];
+      if (t == SS_TIER_RESIDENT) {
+        x.residents.push_back(uint32_t(keys + uint64_t(u)));
+        ++planned;
+      } else if (t == SS_TIER_PINNED) {
+        ++x.P;
+      } else {
+        refuse(SS_E_CAPACITY, "unit (" + std::to_string(l.index) + ", " + std::to_string(u) +
+                                  ") is not resident or pinned (no gated unit is read from its file)");
+      }
+    }
+    x.D += std::min<uint32_t>(b.dynamic_slots_per_layer, uint32_t(l.n_units) - planned);
+    keys += uint64_t(l.n_units);
+    require(keys < 0x7fffffffull, SS_E_INVALID, "device-gated: more than 2^31 - 1 gated units");
+    x.unit_base.push_back(uint32_t(keys));
+  }
+  x.keys = uint32_t(keys);
+  x.R = uint32_t(x.residents.size());
+  if (o.dg_spare_slots) {
+    if (o.dg_spare_slots > x.P)
+      refuse(SS_E_INVALID, "dg_spare_slots " + std::to_string(o.dg_spare_slots) + " above the non-resident units (" +
+                               std::to_string(x.P) + ")");
+    x.D = o.dg_spare_slots;
+  }
+  if (x.D < 1)
+    refuse(SS_E_INVALID, "needs dynamic_slots_per_layer > 0 or dg_spare_slots > 0 (the spare slots)");
+  const uint64_t stride = d.unit_stride(x.gated[0]);
+  uint32_t ring_slots = 0;
+  for (const RingClass& rc : p.rings)
+    if (rc.stride == stride) ring_slots = rc.slots;
+  if (uint64_t(ring_slots) < 2ull * x.B + 1)
+    refuse(SS_E_CAPACITY, "the plan bills " + std::to_string(ring_slots) + " ring slots, the banks and the guard need " +
+                              std::to_string(2 * x.B + 1) + " (set ring_slots = 2 x dg_max_ids + 1)");
+  for (const SpareClass& sc : p.spares)
+    if (sc.block_bytes == x.host_stride) x.Q = sc.blocks;
+  if (x.Q < 1)
+    refuse(SS_E_CAPACITY, "the plan granted no spare blocks (host_spare_units asked " +
+                              std::to_string(b.host_spare_units) + "): a write-back needs a free block");
+  x.blocks = x.P + x.Q;
+  x.persistent_slots = x.R + x.D;
+  const uint64_t S = uint64_t(x.persistent_slots) + 2ull * x.B + 1;
+  require(S < 0x7fffffffull, SS_E_INVALID, "device-gated: more than 2^31 - 1 slots");
+  x.slots = uint32_t(S);
+  x.guard_slot = x.slots - 1;
+  // device admission: what the arena needs in place of what the plan billed for the gated slots
+  uint64_t per_slot = 0;
+  for (uint64_t pb : x.part_bytes) per_slot += pb;
+  const uint64_t need = S * per_slot + keys * 4 + 4096;
+  const uint64_t billed = p.resident + p.dynamic + p.ring;
+  const uint64_t limit = p.cap > p.margin ? p.cap - p.margin : 0;
+  const uint64_t other = p.peak >= billed ? p.peak - billed : 0;
+  if (other + need > limit)
+    refuse(SS_E_CAPACITY, "the arena needs " + std::to_string(need) + " bytes where the plan billed " +
+                              std::to_string(billed) + "; with the rest of the plan that is above the cap - margin");
+  if (p.pinned + x.host_stride + (uint64_t(1) << 20) > b.host_pinned_bytes)
+    refuse(SS_E_CAPACITY, "the plan's pinned bytes plus the staging unit and the mapped control area exceed the host "
+                          "budget (" + std::to_string(b.host_pinned_bytes) + ")");
+  return x;
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// The CUDA mover: copies, entries, ready words and events on the three streams.
+// ---------------------------------------------------------------------------------------------------------------
+class CudaMover final : public Mover {
+ public:
+  struct Buffers {
+    std::vector<char*> arena;     // per part, device
+    std::vector<char*> blocks;    // host addresses (mapped)
+    std::vector<char*> blocks_d;  // the same blocks, device addresses
+    char* staging = nullptr;
+    char* staging_d = nullptr;
+    int32_t* slot_of = nullptr;   // device
+    uint32_t* ready = nullptr;    // device, [G]
+    uint32_t* counters = nullptr; // device, 3 (one per stream)
+  };
+
+  CudaMover(const Layout& x, const Buffers& b) : x_(x), b_(b) {
+    int lo = 0, hi = 0;
+    ck(cudaDeviceGetStreamPriorityRange(&lo, &hi), "cudaDeviceGetStreamPriorityRange");
+    ck(cudaStreamCreateWithPriority(&s_[kDem], cudaStreamNonBlocking, hi), "cudaStreamCreate (demand)");
+    ck(cudaStreamCreateWithPriority(&s_[kPf], cudaStreamNonBlocking, lo), "cudaStreamCreate (prefetch)");
+    ck(cudaStreamCreateWithFlags(&s_[kD2h], cudaStreamNonBlocking), "cudaStreamCreate (write-back)");
+    ck(cudaHostAlloc(reinterpret_cast<void**>(&table_pin_), size_t(std::max<uint32_t>(x_.keys, 1)) * 4,
+                     cudaHostAllocPortable),
+       "cudaHostAlloc (table staging)");
+    for (int i = 0; i < 3; ++i) batch_[i] = std::make_unique<dev::Batch>();
+    // copy engines for parts at least this large (they measured faster there), the land kernel below it;
+    // TSB_COPY_MODE=kernel | ce forces one mover, TSB_CE_MIN_BYTES moves the threshold
+    ce_min_ = uint64_t(8) << 20;
+    if (const char* e = std::getenv("TSB_CE_MIN_BYTES")) ce_min_ = std::strtoull(e, nullptr, 10);
+    if (const char* e = std::getenv("TSB_COPY_MODE")) {
+      if (!std::strcmp(e, "kernel")) ce_min_ = UINT64_MAX;
+      else if (!std::strcmp(e, "ce")) ce_min_ = 0;
+    }
+    deterministic_ = std::getenv("TSB_DG_DETERMINISTIC") && std::getenv("TSB_DG_DETERMINISTIC")[0] == '1';
+  }
+  ~CudaMover() override {
+    for (cudaStream_t s : s_)
+      if (s) cudaStreamSynchronize(s);
+    if (table_pin_) cudaFreeHost(table_pin_);
+    for (cudaStream_t s : s_)
+      if (s) cudaStreamDestroy(s);
+  }
+  cudaStream_t stream(Stream s) const { return s_[s]; }
+  bool deterministic() const { return deterministic_; }
+  bool kernel_copies() const { return ce_min_ > x_.part_bytes[0]; }
+  uint64_t kernel_launches() const { return launches_; }
+
+  uint32_t parts() const override { return uint32_t(x_.part_bytes.size()); }
+  uint64_t part_bytes(uint32_t p) const override { return x_.part_bytes[p]; }
+
+  void h2d(Stream s, int32_t slot, int32_t block) override {
+    for (uint32_t p = 0; p < parts(); ++p)
+      copy(s, block_dev(block) + x_.part_offset[p], arena(p, slot), x_.part_bytes[p], cudaMemcpyHostToDevice);
+  }
+  void d2h(Stream s, int32_t slot, int32_t block, int32_t part) override {
+    for (uint32_t p = 0; p < parts(); ++p) {
+      if (part >= 0 && uint32_t(part) != p) continue;
+      copy(s, arena(p, slot), block_dev(block) + x_.part_offset[p], x_.part_bytes[p], cudaMemcpyDeviceToHost);
+    }
+  }
+  void d2d_moves(const std::vector<std::pair<int32_t, int32_t>>& moves, const std::vector<uint32_t>& wave) override {
+    flush(kDem);
+    uint32_t max_wave = 0;
+    for (uint32_t w : wave) max_wave = std::max(max_wave, w);
+    for (uint32_t w = 0; w <= max_wave; ++w) {  // one or more land launches per wave, stream-ordered on kDem
+      for (size_t i = 0; i < moves.size(); ++i) {
+        if (wave[i] != w) continue;
+        for (uint32_t p = 0; p < parts(); ++p)
+          add_copy(kDem, arena(p, moves[i].first), arena(p, moves[i].second), x_.part_bytes[p]);
+      }
+      flush(kDem);
+    }
+    sync(kDem);
+  }
+  void h2h(int32_t src, int32_t dst) override {
+    std::memcpy(block_host(dst), block_host(src), size_t(x_.unit_bytes));
+  }
+  void publish(Stream s, uint32_t key, int32_t v) override {
+    if (kernel_copies()) {
+      dev::Batch& b = *batch_[s];
+      if (b.n_entries == dev::kMaxEntries) flush(s);
+      b.entry_key[b.n_entries] = key;
+      b.entry_val[b.n_entries] = v;
+      ++b.n_entries;
+      return;
+    }
+    flush(s);
+    ck_drv(write_value32(reinterpret_cast<CUstream>(s_[s]), reinterpret_cast<CUdeviceptr>(b_.slot_of + key),
+                         cuuint32_t(v)),
+           "cuStreamWriteValue32 (entry)");
+  }
+  void ready(uint32_t g, uint32_t seq) override {
+    if (kernel_copies()) {
+      dev::Batch& b = *batch_[kDem];
+      b.ready_word = b_.ready + g;
+      b.ready_val = seq;
+      flush(kDem, true);
+      return;
+    }
+    flush(kDem);
+    ck_drv(write_value32(reinterpret_cast<CUstream>(s_[kDem]), reinterpret_cast<CUdeviceptr>(b_.ready + g),
+                         cuuint32_t(seq)),
+           "cuStreamWriteValue32 (ready)");
+  }
+  void* event_create() override {
+    cudaEvent_t e = nullptr;
+    ck(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "cudaEventCreate");
+    return e;
+  }
+  void event_destroy(void* ev) override {
+    if (ev) cudaEventDestroy(static_cast<cudaEvent_t>(ev));
+  }
+  void record(void* ev, Stream s) override {
+    flush(s);
+    ck(cudaEventRecord(static_cast<cudaEvent_t>(ev), s_[s]), "cudaEventRecord");
+  }
+  void wait(Stream s, void* ev) override {
+    flush(s);
+    ck(cudaStreamWaitEvent(s_[s], static_cast<cudaEvent_t>(ev), 0), "cudaStreamWaitEvent");
+  }
+  bool done(void* ev) override {
+    if (deterministic_) {  // the reference's immediate transport: every event complete when asked
+      ck(cudaEventSynchronize(static_cast<cudaEvent_t>(ev)), "cudaEventSynchronize");
+      return true;
+    }
+    const cudaError_t e = cudaEventQuery(static_cast<cudaEvent_t>(ev));
+    if (e == cudaErrorNotReady) return false;
+    ck(e, "cudaEventQuery");
+    return true;
+  }
+  void event_sync(void* ev) override { ck(cudaEventSynchronize(static_cast<cudaEvent_t>(ev)), "cudaEventSynchronize"); }
+  void sync(Stream s) override {
+    flush(s);
+    ck(cudaStreamSynchronize(s_[s]), "cudaStreamSynchronize");
+  }
+  void upload_table(const int32_t* t, uint32_t n) override {
+    flush(kDem);
+    std::memcpy(table_pin_, t, size_t(n) * 4);
+    ck(cudaMemcpyAsync(b_.slot_of, table_pin_, size_t(n) * 4, cudaMemcpyHostToDevice, s_[kDem]), "cudaMemcpyAsync (table)");
+    ck(cudaStreamSynchronize(s_[kDem]), "cudaStreamSynchronize (table)");
+  }
+  void drain_all() noexcept {
+    for (cudaStream_t s : s_)
+      if (s) cudaStreamSynchronize(s);
+  }
+  void gate(Stream s, cudaEvent_t ev) {
+    flush(s);
+    ck(cudaStreamWaitEvent(s_[s], ev, 0), "cudaStreamWaitEvent (test gate)");
+  }
+
+ private:
+  char* arena(uint32_t p, int32_t slot) const { return b_.arena[p] + uint64_t(slot) * x_.part_bytes[p]; }
+  char* block_dev(int32_t b) const { return b < 0 ? b_.staging_d : b_.blocks_d[size_t(b)]; }
+  char* block_host(int32_t b) const { return b < 0 ? b_.staging : b_.blocks[size_t(b)]; }
+
+  void copy(Stream s, const char* src, char* dst, uint64_t bytes, cudaMemcpyKind kind) {
+    if (bytes >= ce_min_) {
+      flush(s);
+      ck(cudaMemcpyAsync(dst, src, size_t(bytes), kind, s_[s]), "cudaMemcpyAsync (part)");
+      return;
+    }
+    add_copy(s, src, dst, bytes);
+  }
+  void add_copy(Stream s, const char* src, char* dst, uint64_t bytes) {
+    dev::Batch& b = *batch_[s];
+    if (b.n_copies == dev::kMaxCopies) flush(s);
+    b.copies[b.n_copies++] = {src, dst, bytes};
+    chunks_[s] += (bytes + (64u << 10) - 1) >> 16;
+  }
+  void flush(Stream s, bool force = false) {
+    dev::Batch& b = *batch_[s];
+    if (!b.n_copies && !b.n_entries && !b.ready_word && !force) return;
+    b.slot_of = b_.slot_of;
+    b.done_counter = b_.counters + s;
+    const int blocks = int(std::min<uint64_t>(std::max<uint64_t>(chunks_[s], 1), 296));
+    ck_launch(dev::launch_batch(b, blocks, s_[s]), "land kernel");
+    ++launches_;
+    b.n_copies = b.n_entries = 0;
+    b.ready_word = nullptr;
+    chunks_[s] = 0;
+  }
+
+  const Layout& x_;
+  Buffers b_;
+  cudaStream_t s_[3] = {nullptr, nullptr, nullptr};
+  int32_t* table_pin_ = nullptr;
+  std::unique_ptr<dev::Batch> batch_[3];
+  uint64_t chunks_[3] = {0, 0, 0};
+  uint64_t ce_min_ = 0;
+  uint64_t launches_ = 0;
+  bool deterministic_ = false;
+};
+
+// ---------------------------------------------------------------------------------------------------------------
+// The mapped control area: records, flags and words shared with the kernels (host and device addresses).
+// ---------------------------------------------------------------------------------------------------------------
+struct Mapped {
+  dev::DgRecord* rec = nullptr;
+  dev::DgPredRecord* prec = nullptr;
+  uint32_t* flag = nullptr;
+  uint32_t* pflag = nullptr;
+  uint32_t* done = nullptr;
+  uint32_t* err_code = nullptr;
+  uint32_t* err_aux = nullptr;
+  uint32_t* host_abort = nullptr;
+  uint32_t* host_seq = nullptr;
+  uint32_t* began = nullptr;
+  uint32_t* err_count = nullptr;
+};
+
+struct LayerTimes {
+  double seen_us = -1, demand_us = -1, pred_wait_us = -1, prefetch_us = -1, serve_us = -1;
+  uint32_t ids = 0, misses = 0, covered = 0, fetched = 0, prefetched = 0, predicted_true = 0, covered_waits = 0;
+};
+
+// ---------------------------------------------------------------------------------------------------------------
+// The service thread: waits for each exported layer's flag, serves it through the cache, publishes a terminal word.
+// The protocol and its checks follow the reference's DgService (dg_service.cpp:116-365).
+// ---------------------------------------------------------------------------------------------------------------
+class Service {
+ public:
+  enum State : uint32_t { kIdle = 0, kServed = 1, kFailed = 2, kStopped = 3 };
+  Service(SlotCache* core, const Mapped& m, uint32_t max_ids, uint32_t timeout_ms, int device, bool deterministic,
+          bool diag)
+      : core_(core), m_(m), max_ids_(max_ids), timeout_(std::chrono::milliseconds(timeout_ms)), device_(device),
+        deterministic_(deterministic), diag_(diag) {
+    const uint32_t G = core_->gated();
+    run_.assign(G, 1);
+    run_next_.assign(G, 1);
+    last_flag_.assign(G, 0);
+    times_.assign(G, LayerTimes{});
+    ids_.reserve(dev::kMaxIds);
+    pred_.reserve(dev::kMaxIds);
+  }
+  ~Service() { stop_join(); }
+  void start() { th_ = std::thread([this] { run(); }); }
+  void stop_join() {
+    stop_.store(true, std::memory_order_release);
+    if (th_.joinable()) th_.join();
+  }
+  // The engine thread, at ss_begin (release: the run flags, then the sequence).
+  void begin(uint32_t seq, const std::vector<uint8_t>& run) {
+    std::copy(run.begin(), run.end(), run_next_.begin());
+    host_seq_.store(seq, std::memory_order_release);
+  }
+  // Waits (bounded) until the service published a terminal word for seq; returns its state.
+  State wait_terminal(uint32_t seq, std::chrono::milliseconds left) {
+    const auto deadline = Clock::now() + left;
+    for (uint32_t spins = 0;; ++spins) {
+      const uint64_t t = term_.load(std::memory_order_acquire);
+      if (uint32_t(t) == seq && (t >> 32) != kIdle) return State(t >> 32);
+      if ((t >> 32) == kStopped || (t >> 32) == kFailed) return State(t >> 32);
+      if (Clock::now() > deadline) return kIdle;
+      if (spins < 2000) cpu_relax();
+      else std::this_thread::yield();
+    }
+  }
+  std::string error() {
+    std::lock_guard<std::mutex> lk(err_mu_);
+    return err_;
+  }
+  const std::vector<LayerTimes>& times() const { return times_done_; }
+
+ private:
+  struct Stop {};
+  void publish(State s, uint32_t seq) { term_.store(uint64_t(s) << 32 | seq, std::memory_order_release); }
+  void fail_with(const std::string& msg) {
+    {
+      std::lock_guard<std::mutex> lk(err_mu_);
+      if (err_.empty()) err_ = msg;
+    }
+    store_release(m_.host_abort, 1);  // every later wait kernel of the token returns at once
+  }
+  void wait_word(const uint32_t* w, uint32_t seq, const char* what, uint32_t g, bool strict, uint32_t last) {
+    const auto start = Clock::now();
+    for (uint32_t spins = 0;; ++spins) {
+      const uint32_t v = load_acquire(w);
+      if (v == seq) return;
+      if (strict && v != last)
+        fail(SS_E_BACKEND, std::string("device-gated: sequence desync: ") + what + " of gated layer " +
+                               std::to_string(g) + " holds " + std::to_string(v) + " while serving token " +
+                               std::to_string(seq));
+      if ((spins & 4095u) == 0) {
+        if (stop_.load(std::memory_order_acquire)) throw Stop{};
+        if (Clock::now() - start > timeout_)
+          fail(SS_E_BACKEND, std::string("device-gated: ") + what + " of gated layer " + std::to_string(g) +
+                                 " never came (token " + std::to_string(seq) + ")");
+      }
+      cpu_relax();
+    }
+  }
+  void wait_began(uint32_t seq) {
+    for (uint32_t spins = 0;; ++spins) {
+      const uint32_t v = load_acquire(m_.began);
+      if (v == seq) return;
+      if (int32_t(v - seq) > 0)
+        fail(SS_E_BACKEND, "device-gated: sequence desync: a gated step began with seq " + std::to_string(v) +
+                               " while serving token " + std::to_string(seq) +
+                               " (a step ran outside ss_begin / ss_end)");
+      if ((spins & 1023u) == 0) {
+        if (stop_.load(std::memory_order_acquire)) throw Stop{};
+        if (load_acquire(m_.host_abort)) throw Stop{};
+      }
+      if (spins < 20000) cpu_relax();
+      else std::this_thread::yield();
+    }
+  }
+  void serve_token(uint32_t seq) {
+    const uint32_t G = core_->gated();
+    std::copy(run_next_.begin(), run_next_.end(), run_.begin());
+    core_->begin_token(seq);
+    if (diag_) std::fill(times_.begin(), times_.end(), LayerTimes{});
+    wait_began(seq);
+    auto t_prev = Clock::now();
+    for (uint32_t g = 0; g < G; ++g) {
+      if (!run_[g]) continue;
+      uint32_t nx = g + 1;
+      while (nx < G && !run_[nx]) ++nx;
+      wait_word(&m_.flag[g], seq, "export flag", g, true, last_flag_[g]);
+      last_flag_[g] = seq;
+      const auto t_seen = Clock::now();
+      const dev::DgRecord& r = m_.rec[g];
+      require(r.seq == seq, SS_E_BACKEND,
+              "device-gated: sequence desync: the record of gated layer " + std::to_string(g) + " is for token " +
+                  std::to_string(r.seq) + ", serving " + std::to_string(seq));
+      const uint32_t n = r.n_ids, n_pred = r.n_pred_promised;
+      require(n >= 1 && n <= max_ids_, SS_E_BACKEND,
+              "device-gated: gated layer " + std::to_string(g) + " exported " + std::to_string(n) + " ids");
+      require(n_pred <= dev::kMaxIds && (n_pred == 0 || g + 1 < G), SS_E_BACKEND,
+              "device-gated: gated layer " + std::to_string(g) + " promised " + std::to_string(n_pred) +
+                  " predicted ids");
+      const uint64_t mask = uint64_t(r.mask_lo) | uint64_t(r.mask_hi) << 32;
+      ids_.assign(r.ids, r.ids + n);
+      const CacheStats before = core_->stats();
+      core_->serve_demand(g, ids_.data(), n, mask);
+      const auto t_demand = Clock::now();
+      core_->serve_use(g, ids_.data(), n, mask);
+      LayerTimes t;
+      t.seen_us = us_between(t_prev, t_seen);
+      t.demand_us = us_between(t_seen, t_demand);
+      if (n_pred > 0 && run_[g + 1]) {
+        wait_word(&m_.pflag[g], seq, "prediction flag", g, false, 0);
+        const auto t_pw = Clock::now();
+        t.pred_wait_us = us_between(t_demand, t_pw);
+        const dev::DgPredRecord& pr = m_.prec[g];
+        require(pr.n_pred == n_pred, SS_E_BACKEND,
+                "device-gated: gated layer " + std::to_string(g) + " predicted " + std::to_string(pr.n_pred) +
+                    " ids, its export promised " + std::to_string(n_pred));
+        pred_.assign(pr.pred, pr.pred + n_pred);
+        const bool ahead = !deterministic_ && load_acquire(&m_.flag[g + 1]) == seq;
+        core_->serve_prediction(g + 1, pred_.data(), n_pred, ahead);
+        t.prefetch_us = us_between(t_pw, Clock::now());
+      }
+      if (core_->deferred() && nx < G)
+        core_->issue_writebacks(g, [&] { return !deterministic_ && load_acquire(&m_.flag[nx]) == seq; });
+      const auto t_end = Clock::now();
+      t.serve_us = us_between(t_seen, t_end);
+      if (diag_) {
+        const CacheStats& a = core_->stats();
+        t.ids = uint32_t(a.lookups - before.lookups);
+        t.misses = uint32_t(a.misses - before.misses);
+        t.covered = uint32_t(a.covered - before.covered);
+        t.covered_waits = uint32_t(a.covered_waits - before.covered_waits);
+        t.fetched = uint32_t(a.fetched - before.fetched);
+        t.prefetched = uint32_t(a.prefetched - before.prefetched);
+        t.predicted_true = uint32_t(a.predicted_true - before.predicted_true);
+        times_[g] = t;
+      }
+      t_prev = t_end;
+    }
+  }
+  void run() {
+    if (cudaSetDevice(device_) != cudaSuccess) {
+      fail_with("device-gated: the service thread cannot bind the device");
+      publish(kFailed, 0);
+      return;
+    }
+    uint32_t seen = 0;
+    for (;;) {
+      uint32_t seq = 0;
+      for (uint32_t spins = 0;; ++spins) {
+        seq = host_seq_.load(std::memory_order_acquire);
+        if (seq != seen) break;
+        if (stop_.load(std::memory_order_acquire)) {
+          publish(kStopped, seen);
+          return;
+        }
+        if (spins < 20000) cpu_relax();
+        else std::this_thread::yield();
+      }
+      seen = seq;
+      try {
+        serve_token(seq);
+        if (diag_) times_done_ = times_;
+      } catch (const Stop&) {
+        publish(kStopped, seq);
+        return;
+      } catch (const std::exception& e) {
+        fail_with(e.what());
+        publish(kFailed, seq);
+        return;
+      }
+      publish(kServed, seq);
+    }
+  }
+
+  SlotCache* core_;
+  Mapped m_;
+  uint32_t max_ids_;
+  std::chrono::milliseconds timeout_;
+  int device_;
+  bool deterministic_, diag_;
+  std::thread th_;
+  std::atomic<bool> stop_{false};
+  std::atomic<uint32_t> host_seq_{0};
+  std::atomic<uint64_t> term_{0};
+  std::mutex err_mu_;
+  std::string err_;
+  std::vector<uint8_t> run_, run_next_;
+  std::vector<uint32_t> last_flag_, ids_, pred_;
+  std::vector<LayerTimes> times_, times_done_;
+};
+
+// ---------------------------------------------------------------------------------------------------------------
+// The context.
+// ---------------------------------------------------------------------------------------------------------------
+class CudaDgContext final : public DgContext {
+ public:
+  CudaDgContext(const Desc& d, const Plan& p, const ss_options& o) : d_(d), o_(o), x_(make_layout(d, p, o)) {
+    try {
+      init();
+    } catch (...) {
+      close();
+      throw;
+    }
+  }
+  ~CudaDgContext() override { close(); }
+
+  bool poisoned() const override { return poisoned_; }
+  void poison() override { poisoned_ = true; }
+  int n_sources() const override { return int(files_.size()); }
+  bool source_direct(int i) const override { return files_[size_t(i)]->direct(); }
+  int gated_index(int layer) const override {
+    return layer >= 0 && size_t(layer) < x_.ordinal.size() ? x_.ordinal[size_t(layer)] : -1;
+  }
+
+  void begin(const uint32_t* rows, int n_layers) override {
+    require(!in_token_, SS_E_INVALID, "ss_begin: a gated token is already open (call ss_end)");
+    if (rows) require(n_layers == int(d_.layers.size()), SS_E_INVALID, "ss_begin: rows_per_layer must cover every layer");
+    const uint32_t G = uint32_t(x_.gated.size());
+    for (uint32_t g = 0; g < G; ++g) run_[g] = rows ? uint8_t(rows[x_.gated[g]] != 0) : uint8_t(1);
+    // no step ran outside a pair: every word still holds the last token's sequence
+    bool clean = load_acquire(m_.done) == seq_ && load_acquire(m_.began) == seq_;
+    for (uint32_t g = 0; clean && g < G; ++g)
+      clean = int32_t(load_acquire(m_.flag + g) - seq_) <= 0 && int32_t(load_acquire(m_.pflag + g) - seq_) <= 0;
+    if (!clean) {
+      store_release(m_.host_abort, 1);
+      svc_->stop_join();
+      poisoned_ = true;
+      fail(SS_E_BACKEND, "device-gated: sequence desync at ss_begin: a gated step ran outside ss_begin / ss_end (done " +
+                             std::to_string(load_acquire(m_.done)) + ", began " + std::to_string(load_acquire(m_.began)) +
+                             ", last token " + std::to_string(seq_) + "; the context is poisoned)");
+    }
+    ++seq_;
+    in_token_ = true;
+    store_release(m_.host_seq, seq_);
+    svc_->begin(seq_, run_);
+  }
+
+  void end() override {
+    require(in_token_, SS_E_INVALID, "ss_end: no gated token is open");
+    in_token_ = false;
+    const auto deadline = Clock::now() + std::chrono::milliseconds(uint64_t(o_.dg_wait_timeout_ms) + 5000);
+    auto left = [&] {
+      const auto now = Clock::now();
+      return now < deadline ? std::chrono::duration_cast<std::chrono::milliseconds>(deadline - now)
+                            : std::chrono::milliseconds(0);
+    };
+    if (!skip_edge_) {  // the end kernel ran after every reader of the token
+      uint32_t v = 0;
+      for (uint32_t spins = 0;; ++spins) {
+        v = load_acquire(m_.done);
+        if (v == seq_ || int32_t(v - seq_) > 0 || Clock::now() > deadline) break;
+        if (spins < 20000) cpu_relax();
+        else std::this_thread::yield();
+      }
+      const uint32_t began = load_acquire(m_.began);
+      if (v != seq_ || began != seq_) {
+        const std::string dev = device_error();
+        store_release(m_.host_abort, 1);
+        svc_->stop_join();
+        poisoned_ = true;
+        fail(SS_E_BACKEND, token_failure(dev, v == seq_ || int32_t(v - seq_) > 0
+                                                  ? "sequence desync at ss_end: another gated step ran in it"
+                                                  : "the device did not finish it (no end kernel)"));
+      }
+    }
+    const Service::State st = svc_->wait_terminal(seq_, left());
+    if (st != Service::kServed) {
+      const std::string dev = device_error();
+      store_release(m_.host_abort, 1);
+      svc_->stop_join();
+      poisoned_ = true;
+      const std::string why = svc_->error();
+      fail(SS_E_BACKEND, token_failure(dev, "the service: " + (why.empty() ? std::string("it did not finish") : why)));
+    }
+    const std::string dev = device_error();
+    if (!dev.empty()) {
+      poisoned_ = true;
+      fail(SS_E_BACKEND, token_failure(dev, ""));
+    }
+    const auto t0 = Clock::now();
+    core_->end_token(keep_all());
+    boundary_.writebacks = uint32_t(core_->stats().evicted - evicted_before_);
+    evicted_before_ = core_->stats().evicted;
+    boundary_.sync_us = 0;
+    boundary_.select_us = us_between(t0, Clock::now());
+    if (o_.dg_diag) collect_diag();
+    timeline_valid_ = true;
+  }
+
+  void seed(int layer, const int32_t* units, int n) override {
+    require(!in_token_, SS_E_INVALID, "ss_seed: between tokens in device-gated mode");
+    const int g = gated_index(layer);
+    require(g >= 0, SS_E_INVALID, "ss_seed: layer " + std::to_string(layer) + " is not gated");
+    require(n >= 0 && (n == 0 || units), SS_E_INVALID, "ss_seed: bad arguments");
+    std::vector<uint32_t> keys;
+    for (int i = 0; i < n; ++i) {
+      require(units[i] >= 0 && uint32_t(units[i]) < core_->units(uint32_t(g)), SS_E_INVALID, "ss_seed: unit out of range");
+      keys.push_back(core_->key(uint32_t(g), uint32_t(units[i])));
+    }
+    core_->seed(keys);
+  }
+
+  void check_unit(int layer, int unit) override {
+    require(!in_token_, SS_E_INVALID, "ss_check_unit: between tokens in device-gated mode");
+    const int g = gated_index(layer);
+    require(g >= 0, SS_E_INVALID, "ss_check_unit: layer " + std::to_string(layer) + " is not gated");
+    require(unit >= 0 && uint32_t(unit) < core_->units(uint32_t(g)), SS_E_INVALID, "ss_check_unit: unit out of range");
+    core_->drain();
+    const uint32_t k = core_->key(uint32_t(g), uint32_t(unit));
+    std::vector<char> got(size_t(x_.unit_bytes)), want(size_t(x_.unit_bytes));
+    if (core_->slot_of(k) >= 0 &&
+        (core_->home(k) == SlotCache::Home::Device || core_->home(k) == SlotCache::Home::Evicting)) {
+      for (size_t p = 0; p < x_.part_bytes.size(); ++p)
+        ck(cudaMemcpy(got.data() + x_.part_offset[p], bufs_.arena[p] + uint64_t(core_->slot_of(k)) * x_.part_bytes[p],
+                      size_t(x_.part_bytes[p]), cudaMemcpyDeviceToHost),
+           "cudaMemcpy (check)");
+    } else {
+      std::memcpy(got.data(), bufs_.blocks[size_t(core_->block_of(k))], got.size());
+    }
+    read_unit(layer, unit, want.data());
+    require(std::memcmp(got.data(), want.data(), got.size()) == 0, SS_E_HASH,
+            "check_unit: the bytes of (" + std::to_string(layer) + ", " + std::to_string(unit) +
+                ") differ from the source");
+    core_->check();
+  }
+
+  void device_view(ss_dg_device_view* v) const override {
+    std::memset(v, 0, sizeof *v);
+    v->struct_size = uint32_t(sizeof *v);
+    v->protocol = SS_DG_PROTOCOL;
+    v->n_gated = uint32_t(x_.gated.size());
+    v->n_parts = uint32_t(x_.part_bytes.size());
+    v->guard_slot = x_.guard_slot;
+    v->slots = x_.slots;
+    v->slot_of = bufs_.slot_of;
+    v->unit_base = dev_.unit_base;
+    v->abort = dev_.abort;
+    for (size_t p = 0; p < x_.part_bytes.size(); ++p) v->parts[p] = {bufs_.arena[p], x_.part_bytes[p], x_.part_bytes[p]};
+    v->absent_err = dev_.absent_err;
+  }
+
+  void enqueue_begin(void* s) override {
+    require(s != nullptr, SS_E_INVALID, "ss_dg_enqueue_begin: null stream");
+    ck_launch(dev::launch_dg_begin(dev_, s), "begin kernel");
+  }
+  void enqueue_export(int g, const int32_t* ids, int n, int n_pred, void* s) override {
+    require(s && ids, SS_E_INVALID, "ss_dg_enqueue_export: null argument");
+    check_g(g, "ss_dg_enqueue_export");
+    require(n >= 1 && uint32_t(n) <= x_.B, SS_E_INVALID,
+            "ss_dg_enqueue_export: n must be 1..dg_max_ids (" + std::to_string(x_.B) + ")");
+    require(n_pred >= 0 && n_pred <= int(dev::kMaxIds), SS_E_INVALID, "ss_dg_enqueue_export: n_pred must be 0..64");
+    require(n_pred == 0 || uint32_t(g) + 1 < x_.gated.size(), SS_E_INVALID,
+            "ss_dg_enqueue_export: the last gated layer cannot promise a prediction");
+    ck_launch(dev::launch_dg_export(dev_, uint32_t(g), ids, uint32_t(n), uint32_t(n_pred), s), "export kernel");
+  }
+  void enqueue_predict(int g, const int32_t* ids, int n, void* s) override {
+    require(s && ids, SS_E_INVALID, "ss_dg_enqueue_predict: null argument");
+    check_g(g, "ss_dg_enqueue_predict");
+    require(uint32_t(g) + 1 < x_.gated.size(), SS_E_INVALID, "ss_dg_enqueue_predict: the last gated layer has no next");
+    require(n >= 1 && n <= int(dev::kMaxIds), SS_E_INVALID, "ss_dg_enqueue_predict: n must be 1..64");
+    ck_launch(dev::launch_dg_predict(dev_, uint32_t(g), ids, uint32_t(n), s), "predict kernel");
+  }
+  void enqueue_wait(int g, void* s) override {
+    require(s != nullptr, SS_E_INVALID, "ss_dg_enqueue_wait: null stream");
+    check_g(g, "ss_dg_enqueue_wait");
+    ck_launch(dev::launch_dg_wait(dev_, uint32_t(g), s), "wait kernel");
+  }
+  void enqueue_end(void* s) override {
+    require(s != nullptr, SS_E_INVALID, "ss_dg_enqueue_end: null stream");
+    ck_launch(dev::launch_dg_end(dev_, s), "end kernel");
+  }
+
+  void keep(int g, const int32_t* ids, int n) override {
+    require(!in_token_, SS_E_INVALID, "ss_dg_keep: between tokens only");
+    check_g(g, "ss_dg_keep");
+    require(n >= 0 && (n == 0 || ids), SS_E_INVALID, "ss_dg_keep: bad arguments");
+    std::vector<uint32_t> keys;
+    for (int i = 0; i < n; ++i) {
+      require(ids[i] >= 0 && uint32_t(ids[i]) < core_->units(uint32_t(g)), SS_E_INVALID, "ss_dg_keep: unit out of range");
+      keys.push_back(core_->key(uint32_t(g), uint32_t(ids[i])));
+    }
+    keep_[size_t(g)] = std::move(keys);
+  }
+  uint32_t residency(ss_dg_unit* out, uint32_t cap) override {
+    require(!in_token_, SS_E_INVALID, "ss_dg_residency: between tokens only");
+    const std::vector<uint32_t> keys = core_->residency();
+    const uint32_t n = uint32_t(std::min<size_t>(keys.size(), cap));
+    for (uint32_t i = 0; i < n; ++i) {
+      const uint32_t g = core_->gated_of(keys[i]);
+      out[i] = ss_dg_unit{int32_t(g), int32_t(keys[i] - core_->key(g, 0))};
+    }
+    return uint32_t(keys.size());
+  }
+  void set_sched(uint32_t wb_defer, uint32_t flush_ready) override {
+    require(!in_token_, SS_E_INVALID, "ss_dg_set_sched: between tokens only");
+    require(wb_defer <= 1 && flush_ready <= 1, SS_E_INVALID, "ss_dg_set_sched: 0 or 1 each");
+    core_->set_wb_defer(wb_defer != 0);
+  }
+  void set_budgets(uint32_t spare_target, uint32_t per_layer, uint32_t per_token) override {
+    require(!in_token_, SS_E_INVALID, "ss_dg_set_budgets: between tokens only");
+    require(spare_target <= x_.D, SS_E_INVALID,
+            "ss_dg_set_budgets: spare_target above the billed spares (" + std::to_string(x_.D) + ")");
+    core_->set_spare_target(spare_target);
+    core_->set_prefetch_budget(per_layer, per_token);
+  }
+  void timeline(int g, ss_dg_layer_timeline* out) const override {
+    require(!in_token_, SS_E_INVALID, "ss_dg_timeline: between tokens only");
+    require(o_.dg_diag != 0, SS_E_INVALID, "ss_dg_timeline: the context was opened without dg_diag");
+    check_g(g, "ss_dg_timeline");
+    ss_dg_layer_timeline t{};
+    t.struct_size = uint32_t(sizeof t);
+    t.layer = uint32_t(x_.gated[size_t(g)]);
+    t.dma_ms = t.gpu_wait_us = t.gpu_export_ready_us = t.wb_left_ms = t.dma_first_ms = -1;
+    const std::vector<LayerTimes>& tt = svc_->times();
+    if (timeline_valid_ && size_t(g) < tt.size()) {
+      const LayerTimes& l = tt[size_t(g)];
+      t.seen_us = l.seen_us;
+      t.demand_us = l.demand_us;
+      t.pred_wait_us = l.pred_wait_us;
+      t.prefetch_us = l.prefetch_us;
+      t.serve_us = l.serve_us;
+      t.ids = l.ids;
+      t.misses = l.misses;
+      t.covered = l.covered;
+      t.fetched = l.fetched;
+      t.prefetched = l.prefetched;
+      t.predicted_true = l.predicted_true;
+      t.covered_waits = l.covered_waits;
+      t.gpu_wait_us = gpu_wait_us_[size_t(g)];
+      t.gpu_export_ready_us = gpu_ready_us_[size_t(g)];
+    }
+    std::memcpy(out, &t, sizeof t);
+  }
+  void boundary_timeline(ss_dg_boundary_timeline* out) const override {
+    ss_dg_boundary_timeline b = boundary_;
+    b.struct_size = uint32_t(sizeof b);
+    std::memcpy(out, &b, sizeof b);
+  }
+  void stats(ss_dg_stats* out) const override {
+    ss_dg_stats s{};
+    s.struct_size = uint32_t(sizeof s);
+    const CacheStats& c = core_->stats();
+    auto d = [&](uint64_t now, uint64_t base) { return now - base; };
+    s.tokens = d(c.tokens, base_.tokens);
+    s.lookups = d(c.lookups, base_.lookups);
+    s.misses = d(c.misses, base_.misses);
+    s.covered = d(c.covered, base_.covered);
+    s.fetched = d(c.fetched, base_.fetched);
+    s.prefetched = d(c.prefetched, base_.prefetched);
+    s.prefetch_used = d(c.prefetch_used, base_.prefetch_used);
+    s.pred_invalid = d(c.pred_invalid, base_.pred_invalid);
+    s.resurrected = d(c.resurrected, base_.resurrected);
+    s.bank_serves = d(c.bank_serves, base_.bank_serves);
+    s.collected_mid = d(c.collected_mid, base_.collected_mid);
+    s.evicted = d(c.evicted, base_.evicted);
+    s.evict_short = d(c.evict_short, base_.evict_short);
+    s.writebacks_done = d(c.writebacks_done, base_.writebacks_done);
+    s.stalled = d(c.stalled, base_.stalled);
+    s.free_slots = core_->free_slots();
+    s.blocks = x_.blocks;
+    s.slots = x_.slots;
+    s.predicted = d(c.predicted, base_.predicted);
+    s.predicted_true = d(c.predicted_true, base_.predicted_true);
+    s.miss_layers = d(c.miss_layers, base_.miss_layers);
+    s.device_timeouts = *m_.err_count;
+    s.covered_waits = d(c.covered_waits, base_.covered_waits);
+    s.wb_deferred = d(c.wb_deferred, base_.wb_deferred);
+    s.wb_cancelled = d(c.wb_cancelled, base_.wb_cancelled);
+    s.wb_forced = d(c.wb_forced, base_.wb_forced);
+    s.wb_boundary_flushed = d(c.wb_boundary_flushed, base_.wb_boundary_flushed);
+    s.wb_issued_bytes = d(c.wb_issued_bytes, base_.wb_issued_bytes);
+    s.wb_completed_bytes = d(c.wb_completed_bytes, base_.wb_completed_bytes);
+    s.wb_cancelled_bytes = d(c.wb_cancelled_bytes, base_.wb_cancelled_bytes);
+    s.wb_boundary_flushed_bytes = d(c.wb_boundary_flushed_bytes, base_.wb_boundary_flushed_bytes);
+    s.wb_outstanding_bytes = core_->wb_outstanding_bytes();
+    s.wb_forced_wait_ns = d(c.wb_forced_wait_ns, base_.wb_forced_wait_ns);
+    s.cuda_module_loading = module_loading_;
+    std::memcpy(out, &s, sizeof s);
+  }
+  void layer_stats(int layer, ss_layer_stats* out) const override {
+    require(layer >= 0 && size_t(layer) < d_.layers.size(), SS_E_INVALID, "ss_stats_layer: layer out of range");
+    *out = ss_layer_stats{};
+    const int g = gated_index(layer);
+    if (g < 0) return;
+    const LayerCounts& c = core_->layer_counts()[size_t(g)];
+    const LayerCounts& b = lbase_[size_t(g)];
+    out->routed = c.lookups - b.lookups;
+    out->hits = (c.lookups - b.lookups) - (c.misses - b.misses);
+    out->admitted = c.fetched - b.fetched - (c.bank_serves - b.bank_serves);
+    out->transient = c.bank_serves - b.bank_serves;
+    out->evicted = c.evicted - b.evicted;
+    out->prefetched = c.prefetch_used - b.prefetch_used;
+    out->spec_issued = c.prefetched - b.prefetched;
+    out->spec_used = c.prefetch_used - b.prefetch_used;
+    out->bytes_pinned = (c.fetched - b.fetched + c.prefetched - b.prefetched) * x_.unit_bytes;
+  }
+  void total_stats(ss_layer_stats* out) const override {
+    *out = ss_layer_stats{};
+    for (size_t L = 0; L < d_.layers.size(); ++L) {
+      ss_layer_stats s;
+      layer_stats(int(L), &s);
+      out->routed += s.routed;
+      out->hits += s.hits;
+      out->admitted += s.admitted;
+      out->transient += s.transient;
+      out->evicted += s.evicted;
+      out->prefetched += s.prefetched;
+      out->spec_issued += s.spec_issued;
+      out->spec_used += s.spec_used;
+      out->bytes_pinned += s.bytes_pinned;
+    }
+  }
+  void reset_stats() override {
+    base_ = core_->stats();
+    lbase_ = core_->layer_counts();
+  }
+  void exclusive_stats(ss_exclusive_stats* out) const override {
+    ss_exclusive_stats s{};
+    s.struct_size = uint32_t(sizeof s);
+    const CacheStats& c = core_->stats();
+    s.writebacks = c.evicted - c.wb_cancelled;
+    s.writeback_bytes = c.wb_issued_bytes;
+    s.free_blocks = core_->free_blocks();
+    s.min_free_blocks = core_->free_blocks();
+    std::memcpy(out, &s, sizeof s);
+  }
+  std::string stats_json() const override {
+    ss_dg_stats s;
+    stats(&s);
+    char buf[1024];
+    std::snprintf(buf, sizeof buf,
+                  "{\"schema\":\"strix-stream/stats-v1\",\"mode\":\"device-gated\",\"copy\":\"%s\","
+                  "\"dg\":{\"tokens\":%llu,\"lookups\":%llu,\"misses\":%llu,\"covered\":%llu,\"fetched\":%llu,"
+                  "\"prefetched\":%llu,\"bank_serves\":%llu,\"evicted\":%llu,\"resurrected\":%llu,"
+                  "\"writebacks_done\":%llu,\"wb_issued_bytes\":%llu,\"free_slots\":%llu,\"land_launches\":%llu}}",
+                  mover_->kernel_copies() ? "land-kernel" : "copy-engine", (unsigned long long)s.tokens,
+                  (unsigned long long)s.lookups, (unsigned long long)s.misses, (unsigned long long)s.covered,
+                  (unsigned long long)s.fetched, (unsigned long long)s.prefetched, (unsigned long long)s.bank_serves,
+                  (unsigned long long)s.evicted, (unsigned long long)s.resurrected,
+                  (unsigned long long)s.writebacks_done, (unsigned long long)s.wb_issued_bytes,
+                  (unsigned long long)s.free_slots, (unsigned long long)mover_->kernel_launches());
+    return buf;
+  }
+  void reset_open() override {
+    require(!in_token_, SS_E_INVALID, "ss_dg_reset_open: between tokens only");
+    try {
+      core_->reset_open();
+      for (auto& k : keep_) k.clear();
+    } catch (...) {
+      poisoned_ = true;
+      throw;
+    }
+    base_ = core_->stats();
+    lbase_ = core_->layer_counts();
+    timeline_valid_ = false;
+  }
+
+  void test_mutate(int m) override {
+    hooks("ss_test_dg_mutate");
+    require(m >= 0 && m <= 2, SS_E_UNSUPPORTED, "ss_test_dg_mutate: mutation " + std::to_string(m) + " not in this build");
+    core_->set_mutation(m);
+  }
+  void test_pressure(uint32_t f, uint32_t r) override {
+    hooks("ss_test_dg_pressure");
+    core_->set_pressure(f, r);
+  }
+  void test_check() override {
+    hooks("ss_test_dg_check");
+    core_->check();
+  }
+  void test_gate(int stream, void* event) override {
+    hooks("ss_test_dg_gate");
+    require(stream == 0 || stream == 1, SS_E_INVALID, "ss_test_dg_gate: stream 0 or 1");
+    mover_->gate(stream == 0 ? Mover::kDem : Mover::kPf, static_cast<cudaEvent_t>(event));
+  }
+  void test_flags(uint32_t flags) override {
+    hooks("ss_test_dg_flags");
+    dev_.test_flags = flags & dev::kSkipWait;
+    skip_edge_ = (flags & 2u) != 0;
+  }
+  uint32_t test_coming() override {
+    hooks("ss_test_dg_coming");
+    return core_->coming();
+  }
+  void test_stop_service() override {
+    hooks("ss_test_dg_stop_service");
+    svc_->stop_join();
+  }
+  uint32_t test_table(int32_t* out, uint32_t cap) override {
+    hooks("tsb_test_dg_table");
+    require(!in_token_, SS_E_INVALID, "tsb_test_dg_table: between tokens only");
+    require(out && cap >= x_.keys, SS_E_INVALID, "tsb_test_dg_table: the output holds fewer entries than the keys");
+    ck(cudaMemcpy(out, bufs_.slot_of, size_t(x_.keys) * 4, cudaMemcpyDeviceToHost), "cudaMemcpy (table)");
+    return x_.keys;
+  }
+
+ private:
+  void hooks(const char* fn) const {
+    require(o_.dg_test_hooks != 0, SS_E_INVALID, std::string(fn) + ": the context was opened without dg_test_hooks");
+  }
+  void check_g(int g, const char* fn) const {
+    require(g >= 0 && size_t(g) < x_.gated.size(), SS_E_INVALID, std::string(fn) + ": gated layer out of range");
+  }
+  std::vector<uint32_t> keep_all() const {
+    std::vector<uint32_t> all;
+    for (const auto& k : keep_) all.insert(all.end(), k.begin(), k.end());
+    return all;
+  }
+  std::string device_error() const {
+    static const char* names[] = {"", "a wait timed out", "an exported id is out of range", "the host aborted the token",
+                                  "sequence desync (a step the host did not open)", "a lookup met an absent entry"};
+    const uint32_t code = load_acquire(m_.err_code), aux = load_acquire(m_.err_aux);
+    if (!code) return "";
+    return std::string("device: ") + (code < 6 ? names[code] : "unknown error") + " (gated layer / seq " +
+           std::to_string(aux) + ")";
+  }
+  std::string token_failure(const std::string& dev, const std::string& host) const {
+    std::string s = "device-gated: token " + std::to_string(seq_) + " failed: ";
+    if (!dev.empty()) s += dev + (host.empty() ? "" : "; ");
+    return s + host + " (the token's outputs must be discarded; the context is poisoned)";
+  }
+  void collect_diag() {
+    const uint32_t G = uint32_t(x_.gated.size());
+    for (uint32_t g = 0; g < G; ++g) {
+      const volatile unsigned long long* t = stamps_h_ + 4u * g;
+      const unsigned long long ex = t[0], in = t[1], rd = t[2];
+      const bool ok = ex && in && rd && rd >= in && rd >= ex;
+      gpu_wait_us_[g] = ok ? double(rd - in) / 1000.0 : -1;
+      gpu_ready_us_[g] = ok ? double(rd - ex) / 1000.0 : -1;
+    }
+  }
+  char* unit_part_dst(int32_t slot, uint32_t p) const { return bufs_.arena[p] + uint64_t(slot) * x_.part_bytes[p]; }
+  // A gated unit's engine bytes from its source file into dst (parts back to back).
+  void read_unit(int layer, int unit, char* dst) const {
+    const Layer& l = d_.layers[size_t(layer)];
+    uint64_t off = 0;
+    for (const Part& p : l.parts) {
+      files_[size_t(p.source)]->read(dst + off, p.offset + uint64_t(unit) * p.stride, p.bytes);
+      off += p.bytes;
+    }
+  }
+
+  void init() {
+    auto t_start = Clock::now();
+    device_ = o_.device;
+    ck(cudaSetDevice(device_), "cudaSetDevice");
+    ck_launch(dev::preload(), "loading the kernels");
+    CUmoduleLoadingMode mode{};
+    if (driver().loading_mode && driver().loading_mode(&mode) == CUDA_SUCCESS)
+      module_loading_ = mode == CU_MODULE_EAGER_LOADING ? 1u : mode == CU_MODULE_LAZY_LOADING ? 2u : 0u;
+    for (const Source& s : d_.sources) files_.push_back(std::make_unique<SourceFile>(s.path, s.align, o_.direct_io != 0));
+    const uint32_t G = uint32_t(x_.gated.size());
+    // HBM: the arena (guard slot zeroed), the table, the control words
+    for (uint64_t pb : x_.part_bytes) {
+      void* a = nullptr;
+      ck(cudaMalloc(&a, size_t(uint64_t(x_.slots) * pb)), "cudaMalloc (arena)");
+      bufs_.arena.push_back(static_cast<char*>(a));
+      ck(cudaMemset(static_cast<char*>(a) + uint64_t(x_.guard_slot) * pb, 0, size_t(pb)), "cudaMemset (guard slot)");
+    }
+    ck(cudaMalloc(reinterpret_cast<void**>(&bufs_.slot_of), size_t(x_.keys) * 4), "cudaMalloc (slot table)");
+    const size_t ctl_words = 8 + 2 * size_t(G) + (G + 1) + 4;
+    ck(cudaMalloc(reinterpret_cast<void**>(&ctl_), ctl_words * 4), "cudaMalloc (controls)");
+    ck(cudaMemset(ctl_, 0, ctl_words * 4), "cudaMemset (controls)");
+    dev_ = dev::DgDev{};
+    dev_.seq = ctl_;
+    dev_.abort = ctl_ + 1;
+    dev_.err_count = ctl_ + 2;
+    dev_.err_code = ctl_ + 3;
+    dev_.err_aux = ctl_ + 4;
+    dev_.absent_err = ctl_ + 5;
+    bufs_.counters = ctl_ + 8;  // 3 words (one per copy stream)
+    dev_.any_miss = ctl_ + 12;
+    dev_.ready = ctl_ + 12 + G;
+    bufs_.ready = dev_.ready;
+    uint32_t* ub = ctl_ + 12 + 2 * G;
+    ck(cudaMemcpy(ub, x_.unit_base.data(), size_t(G + 1) * 4, cudaMemcpyHostToDevice), "cudaMemcpy (unit_base)");
+    dev_.unit_base = ub;
+    dev_.slot_of = bufs_.slot_of;
+    dev_.timeout_ns = uint64_t(o_.dg_wait_timeout_ms) * 1000000ull;
+    // the mapped control area, 64-byte aligned pieces
+    const size_t rec_b = size_t(G) * sizeof(dev::DgRecord), prec_b = size_t(G) * sizeof(dev::DgPredRecord);
+    auto r64 = [](size_t n) { return (n + 63) / 64 * 64; };
+    const size_t mapped_bytes = r64(rec_b) + r64(prec_b) + 2 * r64(size_t(G) * 4) + 64;
+    ck(cudaHostAlloc(&mapped_h_, mapped_bytes, cudaHostAllocMapped | cudaHostAllocPortable), "cudaHostAlloc (mapped)");
+    std::memset(mapped_h_, 0, mapped_bytes);
+    void* md = nullptr;
+    ck(cudaHostGetDevicePointer(&md, mapped_h_, 0), "cudaHostGetDevicePointer");
+    size_t off = 0;
+    auto carve = [&](size_t bytes, auto** host, auto** devp) {
+      using T = std::remove_pointer_t<std::remove_reference_t<decltype(*host)>>;
+      *host = reinterpret_cast<T*>(static_cast<char*>(mapped_h_) + off);
+      *devp = reinterpret_cast<T*>(static_cast<char*>(md) + off);
+      off += r64(bytes);
+    };
+    carve(rec_b, &m_.rec, &dev_.rec);
+    carve(prec_b, &m_.prec, &dev_.prec);
+    carve(size_t(G) * 4, &m_.flag, &dev_.flag);
+    carve(size_t(G) * 4, &m_.pflag, &dev_.pflag);
+    uint32_t *words_h = nullptr, *words_d = nullptr;
+    carve(7 * 4, &words_h, &words_d);
+    m_.done = words_h;
+    m_.err_code = words_h + 1;
+    m_.err_aux = words_h + 2;
+    m_.host_abort = words_h + 3;
+    m_.host_seq = words_h + 4;
+    m_.began = words_h + 5;
+    m_.err_count = words_h + 6;
+    dev_.done = words_d;
+    dev_.m_err_code = words_d + 1;
+    dev_.m_err_aux = words_d + 2;
+    dev_.host_abort = words_d + 3;
+    dev_.host_seq = words_d + 4;
+    dev_.began = words_d + 5;
+    dev_.m_err_count = words_d + 6;
+    if (o_.dg_diag) {
+      void* h = nullptr;
+      ck(cudaHostAlloc(&h, size_t(G) * 32, cudaHostAllocMapped | cudaHostAllocPortable), "cudaHostAlloc (stamps)");
+      std::memset(h, 0, size_t(G) * 32);
+      stamps_h_ = static_cast<unsigned long long*>(h);
+      void* dd = nullptr;
+      ck(cudaHostGetDevicePointer(&dd, h, 0), "cudaHostGetDevicePointer (stamps)");
+      dev_.stamps = static_cast<unsigned long long*>(dd);
+    }
+    gpu_wait_us_.assign(G, -1);
+    gpu_ready_us_.assign(G, -1);
+    // pinned blocks (mapped: the land kernel reads them), <= 1 GiB chunks; the reset staging unit
+    const uint64_t hs = x_.host_stride;
+    const uint64_t per_chunk = std::max<uint64_t>(1, (uint64_t(1) << 30) / hs);
+    for (uint64_t left = x_.blocks; left > 0;) {
+      const uint64_t n = std::min(per_chunk, left);
+      void* p = nullptr;
+      ck(cudaHostAlloc(&p, size_t(n * hs), cudaHostAllocMapped | cudaHostAllocPortable), "cudaHostAlloc (blocks)");
+      chunks_.push_back(p);
+      void* pd = nullptr;
+      ck(cudaHostGetDevicePointer(&pd, p, 0), "cudaHostGetDevicePointer (blocks)");
+      for (uint64_t i = 0; i < n; ++i) {
+        bufs_.blocks.push_back(static_cast<char*>(p) + i * hs);
+        bufs_.blocks_d.push_back(static_cast<char*>(pd) + i * hs);
+      }
+      left -= n;
+    }
+    ck(cudaHostAlloc(reinterpret_cast<void**>(&bufs_.staging), size_t(hs), cudaHostAllocMapped | cudaHostAllocPortable),
+       "cudaHostAlloc (staging)");
+    void* sd = nullptr;
+    ck(cudaHostGetDevicePointer(&sd, bufs_.staging, 0), "cudaHostGetDevicePointer (staging)");
+    bufs_.staging_d = static_cast<char*>(sd);
+    // the cache: residents in slots 0.., every other unit in a block
+    mover_ = std::make_unique<CudaMover>(x_, bufs_);
+    CacheConfig c;
+    for (int L : x_.gated) c.n_units.push_back(uint32_t(d_.layers[size_t(L)].n_units));
+    c.persistent_slots = x_.persistent_slots;
+    c.bank_slots = x_.B;
+    c.blocks = x_.blocks;
+    const uint32_t T = o_.dg_spare_target == 0xFFFFFFFFu ? x_.D : o_.dg_spare_target;
+    require(T <= x_.D, SS_E_INVALID,
+            "device-gated: dg_spare_target " + std::to_string(T) + " above the billed spares (" + std::to_string(x_.D) + ")");
+    c.spare_target = T;
+    c.prefetch_reserve_auto = o_.dg_prefetch_reserve == 0xFFFFFFFFu;
+    c.prefetch_reserve = c.prefetch_reserve_auto ? std::min<uint32_t>(24, T / 4) : o_.dg_prefetch_reserve;
+    c.prefetch_per_layer = o_.dg_prefetch_per_layer;
+    c.prefetch_per_token = o_.dg_prefetch_per_token;
+    c.wb_defer = o_.dg_wb_defer != 0;
+    c.wb_on_d2h = o_.dg_wb_stream == 1;
+    c.wb_layer_bytes = o_.dg_wb_layer_bytes;
+    c.wb_max_outstanding = o_.dg_wb_max_outstanding;
+    core_ = std::make_unique<SlotCache>(c, mover_.get());
+    std::vector<uint32_t> order;
+    if (o_.dg_seed_n) {
+      require(o_.dg_seed != nullptr, SS_E_INVALID, "device-gated: dg_seed_n > 0 with a null dg_seed");
+      for (uint32_t i = 0; i < o_.dg_seed_n; ++i) {
+        const ss_dg_unit& e = o_.dg_seed[i];
+        require(e.gated >= 0 && uint32_t(e.gated) < G && e.unit >= 0 && uint32_t(e.unit) < core_->units(uint32_t(e.gated)),
+                SS_E_INVALID, "device-gated: dg_seed entry " + std::to_string(i) + " is out of range");
+        order.push_back(core_->key(uint32_t(e.gated), uint32_t(e.unit)));
+      }
+    }
+    o_.dg_seed = nullptr;
+    o_.dg_seed_n = 0;
+    order.insert(order.end(), x_.residents.begin(), x_.residents.end());
+    for (uint32_t k = 0; k < x_.keys; ++k) order.push_back(k);
+    core_->place(order);
+    fill();
+    mover_->upload_table(core_->table().data(), x_.keys);
+    core_->check();
+    keep_.assign(G, {});
+    run_.assign(G, 1);
+    lbase_.assign(G, LayerCounts{});
+    svc_ = std::make_unique<Service>(core_.get(), m_, x_.B, o_.dg_wait_timeout_ms, device_, mover_->deterministic(),
+                                     o_.dg_diag != 0);
+    svc_->start();
+    open_seconds_ = std::chrono::duration<double>(Clock::now() - t_start).count();
+  }
+
+  // The open's fill: every unit's bytes from its file into its slot or block, by a pool of reader threads. A resident
+  // lands through a pinned staging ring; with verify_hash and descriptor hashes, pinned units are hashed on the host
+  // and residents on the device (one K3 launch over every resident slot) before the first token.
+  void fill() {
+    const uint32_t G = uint32_t(x_.gated.size());
+    std::vector<std::pair<uint32_t, uint32_t>> res, pin;  // (g, unit)
+    for (uint32_t g = 0; g < G; ++g)
+      for (uint32_t u = 0; u < core_->units(g); ++u)
+        (core_->slot_of(core_->key(g, u)) >= 0 ? res : pin).push_back({g, u});
+    const bool verify = o_.verify_hash != 0;
+    unsigned nthreads = std::max(1u, std::min(16u, std::thread::hardware_concurrency()));
+    std::atomic<size_t> next{0};
+    std::mutex err_mu;
+    std::string err;
+    auto worker = [&](auto&& job, size_t n) {
+      for (;;) {
+        const size_t i = next.fetch_add(1);
+        if (i >= n) return;
+        try {
+          job(i);
+        } catch (const std::exception& e) {
+          std::lock_guard<std::mutex> lk(err_mu);
+          if (err.empty()) err = e.what();
+        }
+      }
+    };
+    auto run_pool = [&](auto&& job, size_t n) {
+      next = 0;
+      std::vector<std::thread> th;
+      for (unsigned t = 0; t < nthreads; ++t) th.emplace_back([&] { worker(job, n); });
+      for (auto& t : th) t.join();
+      if (!err.empty()) fail(SS_E_IO, err);
+    };
+    auto hash_of = [&](uint32_t g, uint32_t u) -> const uint64_t* {
+      const Layer& l = d_.layers[size_t(x_.gated[g])];
+      return l.hash.empty() ? nullptr : &l.hash[u];
+    };
+    run_pool(
+        [&](size_t i) {
+          const auto [g, u] = pin[i];
+          char* dst = bufs_.blocks[size_t(core_->block_of(core_->key(g, u)))];
+          read_unit(x_.gated[g], int(u), dst);
+          if (verify)
+            if (const uint64_t* h = hash_of(g, u))
+              require(xxh64(dst, size_t(x_.unit_bytes)) == *h, SS_E_HASH,
+                      "device-gated: unit (" + std::to_string(x_.gated[g]) + ", " + std::to_string(u) +
+                          ") differs from its descriptor hash");
+        },
+        pin.size());
+    // residents: through a ring of pinned staging units, nthreads at a time
+    const size_t ring = std::min<size_t>(std::max<size_t>(res.size(), 1), nthreads);
+    std::vector<char*> stage(ring, nullptr);
+    for (auto& s : stage)
+      ck(cudaHostAlloc(reinterpret_cast<void**>(&s), size_t(x_.host_stride), cudaHostAllocPortable), "cudaHostAlloc (fill)");
+    cudaStream_t fs = mover_->stream(Mover::kDem);
+    try {
+      for (size_t first = 0; first < res.size(); first += ring) {
+        const size_t n = std::min(ring, res.size() - first);
+        run_pool([&](size_t i) { read_unit(x_.gated[res[first + i].first], int(res[first + i].second), stage[i]); }, n);
+        for (size_t i = 0; i < n; ++i) {
+          const int32_t slot = core_->slot_of(core_->key(res[first + i].first, res[first + i].second));
+          for (size_t p = 0; p < x_.part_bytes.size(); ++p)
+            ck(cudaMemcpyAsync(unit_part_dst(slot, uint32_t(p)), stage[i] + x_.part_offset[p], size_t(x_.part_bytes[p]),
+                               cudaMemcpyHostToDevice, fs),
+               "cudaMemcpyAsync (fill)");
+        }
+        ck(cudaStreamSynchronize(fs), "cudaStreamSynchronize (fill)");
+      }
+    } catch (...) {
+      for (char* s : stage) cudaFreeHost(s);
+      throw;
+    }
+    for (char* s : stage) cudaFreeHost(s);
+    if (verify && !res.empty() && hash_of(0, 0)) verify_residents(res);
+  }
+
+  // K3 over every resident slot at once: the arena's bytes against the descriptor's hashes.
+  void verify_residents(const std::vector<std::pair<uint32_t, uint32_t>>& res) {
+    const size_t n = res.size();
+    std::vector<dev::HashUnit> units(n);
+    std::vector<uint64_t> expect(n);
+    for (size_t i = 0; i < n; ++i) {
+      const int32_t slot = core_->slot_of(core_->key(res[i].first, res[i].second));
+      dev::HashUnit& h = units[i];
+      h = dev::HashUnit{};
+      h.n_spans = uint32_t(x_.part_bytes.size());
+      for (uint32_t p = 0; p < h.n_spans; ++p) {
+        h.span[p] = reinterpret_cast<const uint8_t*>(unit_part_dst(slot, p));
+        h.bytes[p] = x_.part_bytes[p];
+      }
+      expect[i] = d_.layers[size_t(x_.gated[res[i].first])].hash[res[i].second];
+    }
+    void* buf = nullptr;
+    const size_t bytes = n * (sizeof(dev::HashUnit) + 16) + 16;
+    ck(cudaMalloc(&buf, bytes), "cudaMalloc (verify)");
+    auto* du = static_cast<dev::HashUnit*>(buf);
+    auto* de = reinterpret_cast<uint64_t*>(du + n);
+    auto* dout = de + n;
+    auto* dmis = reinterpret_cast<uint32_t*>(dout + n);
+    cudaStream_t s = mover_->stream(Mover::kDem);
+    uint32_t mism = 0;
+    try {
+      ck(cudaMemcpyAsync(du, units.data(), n * sizeof(dev::HashUnit), cudaMemcpyHostToDevice, s), "verify upload");
+      ck(cudaMemcpyAsync(de, expect.data(), n * 8, cudaMemcpyHostToDevice, s), "verify upload");
+      ck(cudaMemsetAsync(dmis, 0, 4, s), "verify clear");
+      ck_launch(dev::launch_xxh64(du, uint32_t(n), de, dout, nullptr, dmis, s), "xxh64 kernel");
+      ck(cudaMemcpyAsync(&mism, dmis, 4, cudaMemcpyDeviceToHost, s), "verify result");
+      ck(cudaStreamSynchronize(s), "verify sync");
+    } catch (...) {
+      cudaFree(buf);
+      throw;
+    }
+    cudaFree(buf);
+    require(mism == 0, SS_E_HASH,
+            "device-gated: " + std::to_string(mism) + " resident unit(s) differ from their descriptor hashes");
+  }
+
+  void close() noexcept {
+    if (closed_) return;
+    closed_ = true;
+    if (m_.host_abort) store_release(m_.host_abort, 1);
+    if (svc_) svc_->stop_join();
+    if (mover_) mover_->drain_all();
+    cudaDeviceSynchronize();
+    svc_.reset();
+    core_.reset();
+    mover_.reset();
+    for (char* a : bufs_.arena) cudaFree(a);
+    if (bufs_.slot_of) cudaFree(bufs_.slot_of);
+    if (ctl_) cudaFree(ctl_);
+    if (mapped_h_) cudaFreeHost(mapped_h_);
+    if (stamps_h_) cudaFreeHost(stamps_h_);
+    for (void* c : chunks_) cudaFreeHost(c);
+    if (bufs_.staging) cudaFreeHost(bufs_.staging);
+  }
+
+  Desc d_;
+  ss_options o_;
+  Layout x_;
+  int device_ = 0;
+  std::vector<std::unique_ptr<SourceFile>> files_;
+  CudaMover::Buffers bufs_;
+  uint32_t* ctl_ = nullptr;
+  void* mapped_h_ = nullptr;
+  unsigned long long* stamps_h_ = nullptr;
+  std::vector<void*> chunks_;
+  dev::DgDev dev_{};
+  Mapped m_;
+  std::unique_ptr<CudaMover> mover_;
+  std::unique_ptr<SlotCache> core_;
+  std::unique_ptr<Service> svc_;
+  std::vector<std::vector<uint32_t>> keep_;
+  std::vector<uint8_t> run_;
+  uint32_t seq_ = 0;
+  bool in_token_ = false, poisoned_ = false, closed_ = false, skip_edge_ = false, timeline_valid_ = false;
+  uint32_t module_loading_ = 0;
+  CacheStats base_;
+  std::vector<LayerCounts> lbase_;
+  uint64_t evicted_before_ = 0;
+  ss_dg_boundary_timeline boundary_{};
+  std::vector<double> gpu_wait_us_, gpu_ready_us_;
+  double open_seconds_ = 0;
+};
+
+}  // namespace
+
+std::unique_ptr<DgContext> open_dg_context(const Desc& d, const Plan& p, const ss_options& o) {
+  require(o.backend == SS_BACKEND_CUDA, SS_E_UNSUPPORTED,
+          "device-gated: this build has the CUDA backend only (ss_options.backend = SS_BACKEND_CUDA)");
+  return std::make_unique<CudaDgContext>(d, p, o);
+}
+
+}  // namespace tsb

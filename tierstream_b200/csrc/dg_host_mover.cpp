@@ -1,0 +1,145 @@
+// A host mover for the slot cache (dg_core.hpp): the arena and the blocks are host arrays, every copy happens when
+// enqueued, every event is complete when queried. It runs the deterministic replay test hook (tsb_test_dg_replay),
+// which the CPU tests compare with the reference's own DgCore on the same trace; no context uses it.
+#include <cstdio>
+#include <cstring>
+#include <vector>
+
+#include "dg_core.hpp"
+#include "errors.hpp"
+#include "tierstream/tsb.h"
+
+namespace tsb {
+namespace {
+
+class HostMover final : public Mover {
+ public:
+  HostMover(const std::vector<uint64_t>& parts, uint32_t keys, uint32_t slots, uint32_t blocks, bool move)
+      : parts_(parts), table_(keys, -1), move_(move) {
+    for (uint64_t b : parts_) unit_ += b;
+    if (move_) {
+      arena_.assign(size_t(slots) * unit_, 0);
+      blocks_.assign(size_t(blocks) * unit_, 0);
+      stage_.assign(unit_, 0);
+    }
+  }
+  uint8_t* slot_ptr(int32_t s) { return arena_.data() + size_t(s) * unit_; }
+  uint8_t* block_ptr(int32_t b) { return b < 0 ? stage_.data() : blocks_.data() + size_t(b) * unit_; }
+  uint32_t parts() const override { return uint32_t(parts_.size()); }
+  uint64_t part_bytes(uint32_t p) const override { return parts_[p]; }
+  void h2d(Stream, int32_t slot, int32_t block) override {
+    if (move_) std::memcpy(slot_ptr(slot), block_ptr(block), unit_);
+  }
+  void d2h(Stream, int32_t slot, int32_t block, int32_t p) override {
+    if (!move_) return;
+    uint64_t off = 0;
+    for (uint32_t i = 0; i < parts_.size(); ++i) {
+      if (p < 0 || uint32_t(p) == i) std::memcpy(block_ptr(block) + off, slot_ptr(slot) + off, parts_[i]);
+      off += parts_[i];
+    }
+  }
+  void d2d_moves(const std::vector<std::pair<int32_t, int32_t>>& moves, const std::vector<uint32_t>& wave) override {
+    uint32_t top = 0;
+    for (uint32_t w : wave) top = std::max(top, w);
+    for (uint32_t w = 0; w <= top; ++w)
+      for (size_t i = 0; i < moves.size(); ++i)
+        if (wave[i] == w && move_) std::memmove(slot_ptr(moves[i].second), slot_ptr(moves[i].first), unit_);
+  }
+  void h2h(int32_t src, int32_t dst) override {
+    if (move_) std::memmove(block_ptr(dst), block_ptr(src), unit_);
+  }
+  void publish(Stream, uint32_t key, int32_t v) override { table_[key] = v; }
+  void ready(uint32_t, uint32_t) override {}
+  void* event_create() override { return new int(0); }
+  void event_destroy(void* ev) override { delete static_cast<int*>(ev); }
+  void record(void*, Stream) override {}
+  void wait(Stream, void*) override {}
+  bool done(void*) override { return true; }
+  void event_sync(void*) override {}
+  void sync(Stream) override {}
+  void upload_table(const int32_t* t, uint32_t n) override { std::memcpy(table_.data(), t, size_t(n) * 4); }
+
+  std::vector<uint64_t> parts_;
+  std::vector<int32_t> table_;
+  std::vector<uint8_t> arena_, blocks_, stage_;
+  uint64_t unit_ = 0;
+  bool move_;
+};
+
+uint64_t checksum(const uint8_t* p, uint64_t n) {
+  uint64_t s = 0;
+  for (uint64_t i = 0; i < n; ++i) s += uint64_t(p[i]) * (i % 251 + 1);
+  return s;
+}
+
+}  // namespace
+
+void dg_replay(const tsb_dg_replay_config* c, const int32_t* ids, const int32_t* preds, int32_t* tables,
+               uint64_t* stats, const uint8_t* src_units, uint64_t* read_sum) {
+  require(c && c->n_units && c->part_bytes && ids && tables && stats, SS_E_INVALID, "tsb_test_dg_replay: null argument");
+  require(c->n_ids >= 1 && c->n_ids <= 64 && c->n_pred <= 64, SS_E_INVALID, "tsb_test_dg_replay: 1..64 ids");
+  CacheConfig cfg;
+  cfg.n_units.assign(c->n_units, c->n_units + c->n_gated);
+  cfg.persistent_slots = c->persistent_slots;
+  cfg.bank_slots = c->bank_slots;
+  cfg.blocks = c->blocks;
+  cfg.spare_target = c->spare_target;
+  cfg.prefetch_reserve_auto = c->prefetch_reserve == 0xFFFFFFFFu;
+  cfg.prefetch_reserve = cfg.prefetch_reserve_auto ? 0 : c->prefetch_reserve;
+  cfg.prefetch_per_layer = c->prefetch_per_layer;
+  cfg.prefetch_per_token = c->prefetch_per_token;
+  cfg.wb_defer = c->wb_defer != 0;
+  cfg.wb_on_d2h = c->wb_on_d2h != 0;
+  cfg.wb_layer_bytes = c->wb_layer_bytes;
+  cfg.wb_max_outstanding = c->wb_max_outstanding;
+  uint32_t keys = 0;
+  for (uint32_t g = 0; g < c->n_gated; ++g) keys += c->n_units[g];
+  HostMover m(std::vector<uint64_t>(c->part_bytes, c->part_bytes + c->n_parts), keys,
+              c->persistent_slots + 2 * c->bank_slots + 1, c->blocks, c->move_bytes != 0);
+  SlotCache core(cfg, &m);
+  std::vector<uint32_t> order(c->order, c->order + c->n_order);
+  for (uint32_t k = 0; k < keys; ++k) order.push_back(k);
+  core.place(order);
+  m.upload_table(core.table().data(), keys);
+  if (m.move_ && src_units)
+    for (uint32_t k = 0; k < keys; ++k) {
+      uint8_t* dst = core.slot_of(k) >= 0 ? m.slot_ptr(core.slot_of(k)) : m.block_ptr(core.block_of(k));
+      std::memcpy(dst, src_units + size_t(k) * m.unit_, m.unit_);
+    }
+  std::vector<uint32_t> row(c->n_ids), pred(c->n_pred);
+  for (uint32_t t = 0; t < c->tokens; ++t) {
+    core.begin_token(t + 1);
+    for (uint32_t g = 0; g < c->n_gated; ++g) {
+      const int32_t* r = ids + (size_t(t) * c->n_gated + g) * c->n_ids;
+      uint64_t mask = 0;
+      for (uint32_t i = 0; i < c->n_ids; ++i) {  // the export kernel's rule on the device table
+        row[i] = uint32_t(r[i]);
+        if (row[i] < c->n_units[g] && m.table_[core.key(g, row[i])] < 0) mask |= 1ull << i;
+      }
+      core.serve_demand(g, row.data(), c->n_ids, mask);
+      if (read_sum && m.move_)
+        for (uint32_t i = 0; i < c->n_ids; ++i) {
+          const int32_t s = m.table_[core.key(g, row[i])];
+          read_sum[(size_t(t) * c->n_gated + g) * c->n_ids + i] = s < 0 ? 0 : checksum(m.slot_ptr(s), m.unit_);
+        }
+      core.serve_use(g, row.data(), c->n_ids, mask);
+      if (preds && c->n_pred && g + 1 < c->n_gated) {
+        const int32_t* p = preds + (size_t(t) * c->n_gated + g) * c->n_pred;
+        for (uint32_t i = 0; i < c->n_pred; ++i) pred[i] = uint32_t(p[i]);
+        core.serve_prediction(g + 1, pred.data(), c->n_pred, false);
+      }
+      if (core.deferred() && g + 1 < c->n_gated) core.issue_writebacks(g, [] { return false; });
+    }
+    core.end_token({});
+    std::memcpy(tables + size_t(t) * keys, m.table_.data(), size_t(keys) * 4);
+    const CacheStats& s = core.stats();
+    const uint64_t v[16] = {s.tokens,        s.lookups,     s.misses,          s.covered,     s.fetched,
+                            s.prefetched,    s.prefetch_used, s.resurrected,   s.bank_serves, s.collected_mid,
+                            s.evicted,       s.evict_short, s.writebacks_done, s.wb_deferred, s.wb_cancelled,
+                            s.wb_forced};
+    std::memcpy(stats + size_t(t) * 16, v, sizeof v);
+    core.check();
+  }
+}
+
+}  // namespace tsb

@@ -1,0 +1,199 @@
+// A minimal stand-in for an inference engine's decode step (tests and bench.py): it drives a device-gated context
+// through the public ABI exactly as an engine would. Per token, captured once into a CUDA graph on the caller's
+// stream: ss_dg_enqueue_begin, then per gated layer ss_dg_enqueue_export of that layer's routed ids (read from a device
+// buffer the host refills before each launch), ss_dg_enqueue_wait, and a reader kernel that resolves every id through
+// ss_dg_slot (the engine-side inline of ss.h) and reads the whole unit, as a batch-1 MoE matvec reads its experts;
+// then ss_dg_enqueue_end. The reader's result per (layer, id) is a checksum of the unit's bytes:
+//   mode 0: sum(byte * (pos % 251 + 1)) over the unit (the reference GPU tests' check, tests/test_dg_cuda.cu:103-114);
+//   mode 1: the sum of the unit's 32-bit little-endian words (a read at HBM speed, the bench's engine work).
+// This library is not part of the runtime (libtierstream.so never links it).
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <cstring>
+#include <thread>
+#include <vector>
+
+#include "strix_stream/ss.h"
+
+namespace {
+
+constexpr int kThreads = 256;
+
+__device__ __forceinline__ uint64_t warp_sum(uint64_t v) {
+  for (int o = 16; o; o >>= 1) v += __shfl_down_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// grid (n, slices): block (i, s) reads slice s of unit ids[i] of gated layer g and adds its part of the checksum.
+__global__ __launch_bounds__(kThreads) void reader_kernel(ss_dg_device_view v, uint32_t g, const int32_t* ids,
+                                                          uint32_t n, unsigned long long* out, int mode) {
+  const uint32_t i = blockIdx.x;
+  if (i >= n) return;
+  const int32_t slot = ss_dg_slot(&v, g, ids[i]);
+  uint64_t unit_bytes = 0;
+  for (uint32_t p = 0; p < v.n_parts; ++p) unit_bytes += v.parts[p].bytes;
+  // slices of 16-byte vectors; every part is a multiple of 256 bytes in a gated layout
+  const uint64_t n16 = unit_bytes / 16;
+  const uint64_t per = (n16 + gridDim.y - 1) / gridDim.y;
+  const uint64_t lo = per * blockIdx.y, hi = lo + per < n16 ? lo + per : n16;
+  uint64_t acc = 0;
+  for (uint64_t e = lo + threadIdx.x; e < hi; e += kThreads) {
+    uint64_t pos = e * 16;  // position in the unit's bytes
+    uint32_t p = 0;
+    uint64_t off = pos;
+    while (p + 1 < v.n_parts && off >= v.parts[p].bytes) {
+      off -= v.parts[p].bytes;
+      ++p;
+    }
+    const uint4 w = *reinterpret_cast<const uint4*>(static_cast<const char*>(v.parts[p].base) +
+                                                    uint64_t(slot) * v.parts[p].stride + off);
+    if (mode == 1) {
+      acc += uint64_t(w.x) + w.y + w.z + w.w;
+      continue;
+    }
+    const uint32_t words[4] = {w.x, w.y, w.z, w.w};
+    uint32_t m = uint32_t(pos % 251);
+#pragma unroll
+    for (int k = 0; k < 16; ++k) {
+      acc += uint64_t((words[k >> 2] >> (8 * (k & 3))) & 0xffu) * (m + 1);
+      m = m + 1 == 251 ? 0 : m + 1;
+    }
+  }
+  __shared__ uint64_t part[kThreads / 32];
+  acc = warp_sum(acc);
+  if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = acc;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    uint64_t s = 0;
+    for (int k = 0; k < kThreads / 32; ++k) s += part[k];
+    atomicAdd(out + i, (unsigned long long)s);
+  }
+}
+
+#define CK(x)                                  \
+  do {                                         \
+    const cudaError_t e_ = (x);                \
+    if (e_ != cudaSuccess) return int(e_);     \
+  } while (0)
+#define SS(x)                                  \
+  do {                                         \
+    const ss_status s_ = (x);                  \
+    if (s_ != SS_OK) return 1000 + int(s_);    \
+  } while (0)
+
+}  // namespace
+
+extern "C" {
+
+// Captures one token step into a graph on `stream`: for gated layer g its n_ids ids are ids_dev[g * n_ids ..], its
+// results out_dev[g * n_ids ..] (zeroed by the graph first). slices: blocks per unit for the reader. n_pred > 0: each
+// layer g < G - 1 also predicts layer g + 1 from pred_dev[g * n_pred ..] on a forked branch joined before the next
+// export. Returns 0 or an error (cudaError_t, or 1000 + ss_status) and the instantiated graph in *exec_out.
+__attribute__((visibility("default"))) int tse_capture_token(ss_ctx* c, uint32_t n_gated, const int32_t* ids_dev,
+                                                             uint32_t n_ids, const int32_t* pred_dev, uint32_t n_pred,
+                                                             unsigned long long* out_dev, uint32_t slices, int mode,
+                                                             int with_reader, void* stream, void** exec_out) {
+  ss_dg_device_view v;
+  SS(ss_dg_get_device_view(c, &v));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaStream_t side = nullptr;
+  cudaEvent_t fork = nullptr, join = nullptr;
+  if (n_pred) {
+    CK(cudaStreamCreateWithFlags(&side, cudaStreamNonBlocking));
+    CK(cudaEventCreateWithFlags(&fork, cudaEventDisableTiming));
+    CK(cudaEventCreateWithFlags(&join, cudaEventDisableTiming));
+  }
+  cudaGraph_t graph = nullptr;
+  CK(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
+  int err = 0;
+  do {
+    if (with_reader && cudaMemsetAsync(out_dev, 0, size_t(n_gated) * n_ids * 8, s) != cudaSuccess) {
+      err = 1;
+      break;
+    }
+    if (ss_dg_enqueue_begin(c, s) != SS_OK) {
+      err = 1001;
+      break;
+    }
+    for (uint32_t g = 0; g < n_gated && !err; ++g) {
+      const int np = (n_pred && g + 1 < n_gated) ? int(n_pred) : 0;
+      if (ss_dg_enqueue_export(c, int(g), ids_dev + size_t(g) * n_ids, int(n_ids), np, s) != SS_OK) err = 1002;
+      if (!err && np) {
+        if (cudaEventRecord(fork, s) != cudaSuccess || cudaStreamWaitEvent(side, fork, 0) != cudaSuccess) err = 2;
+        if (!err && ss_dg_enqueue_predict(c, int(g), pred_dev + size_t(g) * n_pred, np, side) != SS_OK) err = 1003;
+      }
+      if (!err && ss_dg_enqueue_wait(c, int(g), s) != SS_OK) err = 1004;
+      if (!err && with_reader) {
+        reader_kernel<<<dim3(n_ids, slices), kThreads, 0, s>>>(v, g, ids_dev + size_t(g) * n_ids, n_ids,
+                                                              out_dev + size_t(g) * n_ids, mode);
+        if (cudaGetLastError() != cudaSuccess) err = 3;
+      }
+      if (!err && np) {
+        if (cudaEventRecord(join, side) != cudaSuccess || cudaStreamWaitEvent(s, join, 0) != cudaSuccess) err = 4;
+      }
+    }
+    if (!err && ss_dg_enqueue_end(c, s) != SS_OK) err = 1005;
+  } while (false);
+  const cudaError_t ec = cudaStreamEndCapture(s, &graph);
+  if (side) cudaStreamDestroy(side);
+  if (fork) cudaEventDestroy(fork);
+  if (join) cudaEventDestroy(join);
+  if (err) {
+    if (graph) cudaGraphDestroy(graph);
+    return err;
+  }
+  CK(ec);
+  cudaGraphExec_t exec = nullptr;
+  const cudaError_t ei = cudaGraphInstantiate(&exec, graph, 0);
+  cudaGraphDestroy(graph);
+  CK(ei);
+  *exec_out = exec;
+  return 0;
+}
+
+// The synthetic byte stream of the benchmark's model files: byte i of file `file_id` (the reference fixtures'
+// generator, tests/fixture.hpp:16-22), n bytes from position `first`, on `threads` host threads.
+__attribute__((visibility("default"))) void tse_fill_bytes(uint64_t file_id, uint64_t first, uint64_t n, uint8_t* out,
+                                                           uint32_t threads) {
+  if (threads < 1) threads = 1;
+  auto fill = [=](uint64_t lo, uint64_t hi) {
+    for (uint64_t j = lo; j < hi; ++j) {
+      const uint64_t i = first + j;
+      uint64_t x = (i + 1) * 0x9E3779B97F4A7C15ULL ^ (file_id + 7) * 0xC2B2AE3D27D4EB4FULL;
+      x ^= x >> 29;
+      x *= 0xBF58476D1CE4E5B9ULL;
+      x ^= x >> 32;
+      out[j] = uint8_t(x);
+    }
+  };
+  std::vector<std::thread> th;
+  const uint64_t per = (n + threads - 1) / threads;
+  for (uint32_t t = 0; t < threads; ++t) {
+    const uint64_t lo = per * t, hi = lo + per < n ? lo + per : n;
+    if (lo < hi) th.emplace_back(fill, lo, hi);
+  }
+  for (auto& t : th) t.join();
+}
+
+__attribute__((visibility("default"))) int tse_launch(void* exec, void* stream) {
+  return int(cudaGraphLaunch(static_cast<cudaGraphExec_t>(exec), static_cast<cudaStream_t>(stream)));
+}
+
+__attribute__((visibility("default"))) int tse_destroy(void* exec) {
+  return int(cudaGraphExecDestroy(static_cast<cudaGraphExec_t>(exec)));
+}
+
+// The reader alone (no capture): checksums of n units of gated layer g resolved through the context's table.
+__attribute__((visibility("default"))) int tse_read_units(ss_ctx* c, uint32_t g, const int32_t* ids_dev, uint32_t n,
+                                                          unsigned long long* out_dev, uint32_t slices, int mode,
+                                                          void* stream) {
+  ss_dg_device_view v;
+  SS(ss_dg_get_device_view(c, &v));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  CK(cudaMemsetAsync(out_dev, 0, size_t(n) * 8, s));
+  reader_kernel<<<dim3(n, slices), kThreads, 0, s>>>(v, g, ids_dev, n, out_dev, mode);
+  return int(cudaGetLastError());
+}
+
+}  // extern "C"

@@ -1,0 +1,102 @@
+// The library's device kernels (kernels.cu, sm_100a) and their launchers. Every launcher only enqueues on the given
+// stream (legal during stream capture), allocates nothing and returns the launch's cudaError_t as an int.
+#pragma once
+
+#include <cstdint>
+
+namespace tsb {
+namespace dev {
+
+// ---- K1 / K4 / K5: batched copies ----
+// One copy: `bytes` from src to dst; either side may be device memory, mapped pinned host memory or a peer GPU's
+// memory (P2P). A batch's copies must not overlap each other.
+struct Copy {
+  const void* src;
+  void* dst;
+  uint64_t bytes;
+};
+// Entries published after every copy of the batch landed: slot_of[key] = val (release at system scope), then
+// *ready_word = ready_val when ready_word is set. done_counter: one device word per stream the batches run on (the
+// last block to finish publishes and rezeroes it).
+constexpr uint32_t kMaxCopies = 384;
+constexpr uint32_t kMaxEntries = 128;
+struct Batch {
+  uint32_t n_copies = 0, n_entries = 0;
+  int32_t* slot_of = nullptr;
+  uint32_t* ready_word = nullptr;
+  uint32_t ready_val = 0;
+  uint32_t* done_counter = nullptr;
+  Copy copies[kMaxCopies];
+  uint32_t entry_key[kMaxEntries];
+  int32_t entry_val[kMaxEntries];
+};
+int launch_batch(const Batch& b, int blocks, void* stream);
+
+// ---- K3: device xxh64 of whole units ----
+// A unit is up to 4 spans hashed back to back (a gated unit's parts in the arena). out[i] = the hash; when expect is
+// given, a mismatch increments *mismatches and sets bad[i] = 1 (bad may be null).
+struct HashUnit {
+  const uint8_t* span[4];
+  uint64_t bytes[4];
+  uint32_t n_spans;
+  uint32_t pad;
+};
+int launch_xxh64(const HashUnit* units_dev, uint32_t n, const uint64_t* expect_dev, uint64_t* out_dev,
+                 uint32_t* bad_dev, uint32_t* mismatches_dev, void* stream);
+
+// ---- K2: device-gated decode control kernels ----
+// The record an export writes for the service (mapped host memory); the layout is the reference's DgRecord
+// (dg_proto.hpp:15-25): 288 bytes.
+constexpr uint32_t kMaxIds = 64;
+struct DgRecord {
+  uint32_t n_ids, n_pred_promised, mask_lo, mask_hi;
+  uint32_t seq, pad[3];
+  uint32_t ids[kMaxIds];
+};
+struct DgPredRecord {
+  uint32_t n_pred, pad[3];
+  uint32_t pred[kMaxIds];
+};
+static_assert(sizeof(DgRecord) == 288 && sizeof(DgPredRecord) == 272, "record layout");
+enum DgErr : uint32_t { kDgOk = 0, kDgTimeout = 1, kDgBadId = 2, kDgHostAbort = 3, kDgDesync = 4, kDgAbsent = 5 };
+constexpr uint32_t kSkipWait = 1;  // test mutation: the wait kernel returns at once
+
+// Every pointer the control kernels use, fixed at open (captured graphs replay for the context's life).
+struct DgDev {
+  // device memory
+  uint32_t* seq;
+  uint32_t* abort;
+  uint32_t* err_count;
+  uint32_t* err_code;
+  uint32_t* err_aux;
+  uint32_t* any_miss;    // [G]
+  uint32_t* ready;       // [G], written after a layer's copies and entries
+  uint32_t* absent_err;
+  const int32_t* slot_of;
+  const uint32_t* unit_base;  // [G + 1]
+  // mapped host memory (device addresses)
+  DgRecord* rec;
+  DgPredRecord* prec;
+  uint32_t* flag;
+  uint32_t* pflag;
+  uint32_t* done;
+  uint32_t* m_err_code;
+  uint32_t* m_err_aux;
+  uint32_t* host_abort;
+  uint32_t* host_seq;
+  uint32_t* began;
+  uint32_t* m_err_count;
+  unsigned long long* stamps;  // diag: [4g] export, [4g + 1] wait entry, [4g + 2] ready seen; null = off
+  unsigned long long timeout_ns;
+  uint32_t test_flags;
+};
+int launch_dg_begin(const DgDev& d, void* stream);
+int launch_dg_export(const DgDev& d, uint32_t g, const int32_t* ids, uint32_t n, uint32_t n_pred, void* stream);
+int launch_dg_predict(const DgDev& d, uint32_t g, const int32_t* ids, uint32_t n, void* stream);
+int launch_dg_wait(const DgDev& d, uint32_t g, void* stream);
+int launch_dg_end(const DgDev& d, void* stream);
+// Loads every kernel of this file (no lazy module load inside a capture).
+int preload();
+
+}  // namespace dev
+}  // namespace tsb

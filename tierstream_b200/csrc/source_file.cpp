@@ -1,0 +1,88 @@
+#include "source_file.hpp"
+
+#include <fcntl.h>
+#include <sys/stat.h>
+#include <unistd.h>
+
+#include <cerrno>
+#include <cstdlib>
+#include <cstring>
+#include <memory>
+
+#include "errors.hpp"
+
+namespace tsb {
+
+SourceFile::SourceFile(const std::string& path, uint64_t align, bool direct) : path_(path), align_(align) {
+  fd_buffered_ = ::open(path.c_str(), O_RDONLY | O_CLOEXEC);
+  require(fd_buffered_ >= 0, SS_E_IO, "cannot open source " + path + ": " + std::strerror(errno));
+  struct stat st {};
+  require(::fstat(fd_buffered_, &st) == 0, SS_E_IO, "cannot stat source " + path);
+  size_ = uint64_t(st.st_size);
+  if (direct) {
+    fd_ = ::open(path.c_str(), O_RDONLY | O_CLOEXEC | O_DIRECT);
+    direct_ = fd_ >= 0;  // a file system that refuses O_DIRECT (tmpfs) reads buffered
+  }
+}
+
+SourceFile::~SourceFile() {
+  if (fd_ >= 0) ::close(fd_);
+  if (fd_buffered_ >= 0) ::close(fd_buffered_);
+}
+
+namespace {
+void pread_all(int fd, char* dst, uint64_t off, uint64_t n, const std::string& path) {
+  while (n) {
+    const ssize_t r = ::pread(fd, dst, size_t(n), off_t(off));
+    if (r < 0 && errno == EINTR) continue;
+    require(r > 0, SS_E_IO, "short read of " + path + " at offset " + std::to_string(off));
+    dst += r;
+    off += uint64_t(r);
+    n -= uint64_t(r);
+  }
+}
+}  // namespace
+
+void SourceFile::read(void* dst, uint64_t offset, uint64_t bytes) const {
+  require(offset <= size_ && bytes <= size_ - offset, SS_E_IO,
+          "read past the end of " + path_ + " (offset " + std::to_string(offset) + ", bytes " + std::to_string(bytes) +
+              ")");
+  if (!bytes) return;
+  if (!direct_) {
+    pread_all(fd_buffered_, static_cast<char*>(dst), offset, bytes, path_);
+    return;
+  }
+  // unbuffered: aligned covering reads through a bounce buffer (at most 8 MiB per read)
+  const uint64_t a = align_ < 4096 ? 4096 : align_;
+  const uint64_t piece = uint64_t(8) << 20;
+  void* raw = nullptr;
+  require(::posix_memalign(&raw, size_t(a), size_t(piece + 2 * a)) == 0, SS_E_NOMEM, "bounce buffer");
+  std::unique_ptr<void, decltype(&std::free)> bounce(raw, &std::free);
+  char* out = static_cast<char*>(dst);
+  uint64_t pos = offset, left = bytes;
+  while (left) {
+    const uint64_t start = pos / a * a, skip = pos - start;
+    const uint64_t want = std::min<uint64_t>(left, piece);
+    uint64_t span = (skip + want + a - 1) / a * a;
+    if (start + span > (size_ + a - 1) / a * a) span = (size_ + a - 1) / a * a - start;
+    ssize_t got = 0;
+    while (uint64_t(got) < skip + want) {
+      const ssize_t r = ::pread(fd_, static_cast<char*>(raw) + got, size_t(span - uint64_t(got)), off_t(start + uint64_t(got)));
+      if (r < 0 && errno == EINTR) continue;
+      if (r < 0 && errno == EINVAL) {  // refused after all: buffered for this piece
+        pread_all(fd_buffered_, out, pos, want, path_);
+        got = ssize_t(skip + want);
+        std::memcpy(static_cast<char*>(raw) + skip, out, size_t(want));
+        break;
+      }
+      require(r > 0, SS_E_IO, "short read of " + path_ + " at offset " + std::to_string(start + uint64_t(got)));
+      got += r;
+    }
+    std::memcpy(out, static_cast<char*>(raw) + skip, size_t(want));
+    out += want;
+    pos += want;
+    left -= want;
+  }
+}
+
+}  // namespace tsb

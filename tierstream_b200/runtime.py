@@ -1,0 +1,196 @@
+"""Python handles over the C ABI, in the reference's vocabulary: a descriptor, a plan, a context.
+
+These are thin owners of the library's opaque handles (ss_desc*, ss_plan*, ss_ctx*); every operation is the C call.
+"""
+import ctypes as C
+
+import numpy as np
+
+from . import abi
+
+
+class Desc:
+    def __init__(self, json_text):
+        lib = abi.load()
+        self.h = C.c_void_p()
+        raw = json_text.encode()
+        abi.check(lib.ss_desc_from_json(raw, len(raw), C.byref(self.h)))
+
+    def __del__(self):
+        if getattr(self, "h", None):
+            abi.load().ss_desc_free(self.h)
+            self.h = None
+
+    @property
+    def n_layers(self):
+        return abi.load().ss_desc_n_layers(self.h)
+
+    def layer_units(self, layer):
+        return abi.load().ss_desc_layer_units(self.h, layer)
+
+    def total_units(self):
+        return abi.load().ss_desc_total_units(self.h)
+
+    def to_json(self):
+        p, n = C.c_void_p(), C.c_size_t()
+        abi.check(abi.load().ss_desc_to_json(self.h, C.byref(p), C.byref(n)))
+        return abi.take_text(p, n.value)
+
+
+class Plan:
+    def __init__(self, desc, budget, tiers=None, benefit=None):
+        lib = abi.load()
+        self.desc = desc
+        self.budget = budget
+        self.h = C.c_void_p()
+        if tiers is not None:
+            t = (C.c_uint8 * len(tiers))(*tiers)
+            abi.check(lib.ss_plan_from_tiers(desc.h, C.byref(budget), t, len(tiers), C.byref(self.h)))
+        else:
+            b = (C.c_double * len(benefit))(*benefit) if benefit is not None else None
+            abi.check(lib.ss_plan_make(desc.h, C.byref(budget), b, len(benefit) if benefit is not None else 0,
+                                       C.byref(self.h)))
+
+    def __del__(self):
+        if getattr(self, "h", None):
+            abi.load().ss_plan_free(self.h)
+            self.h = None
+
+    def to_json(self):
+        p, n = C.c_void_p(), C.c_size_t()
+        abi.check(abi.load().ss_plan_to_json(self.h, C.byref(p), C.byref(n)))
+        return abi.take_text(p, n.value)
+
+    def totals(self):
+        t = abi.ss_plan_totals()
+        abi.load().ss_plan_get_totals(self.h, C.byref(t))
+        return {n: getattr(t, n) for n, _ in t._fields_}
+
+
+class DgContext:
+    """A device-gated context (ss_open with forward_mode = SS_FORWARD_DEVICE_GATED)."""
+
+    def __init__(self, desc, plan, options):
+        lib = abi.load()
+        self.desc, self.plan = desc, plan
+        self.h = C.c_void_p()
+        abi.check(lib.ss_open(desc.h, C.byref(plan.budget), plan.h, C.byref(options), C.byref(self.h)))
+
+    def close(self):
+        if getattr(self, "h", None):
+            abi.load().ss_close(self.h)
+            self.h = None
+
+    def __del__(self):
+        self.close()
+
+    def begin(self):
+        abi.check(abi.load().ss_begin(self.h, None, 0))
+
+    def end(self):
+        abi.check(abi.load().ss_end(self.h))
+
+    def view(self):
+        v = abi.ss_dg_device_view()
+        abi.check(abi.load().ss_dg_get_device_view_sized(self.h, C.byref(v), C.sizeof(v)))
+        return v
+
+    def stats(self):
+        s = abi.ss_dg_stats()
+        abi.check(abi.load().ss_stats_dg_sized(self.h, C.byref(s), C.sizeof(s)))
+        return {n: getattr(s, n) for n, _ in s._fields_}
+
+    def stats_json(self):
+        p, n = C.c_void_p(), C.c_size_t()
+        abi.check(abi.load().ss_stats_to_json(self.h, C.byref(p), C.byref(n)))
+        return abi.take_text(p, n.value)
+
+    def table(self, keys):
+        out = np.empty(keys, dtype=np.int32)
+        abi.check(abi.load().tsb_test_dg_table(self.h, out.ctypes.data_as(C.POINTER(C.c_int32)), keys))
+        return out
+
+    def check(self):
+        abi.check(abi.load().ss_test_dg_check(self.h))
+
+    def check_unit(self, layer, unit):
+        abi.check(abi.load().ss_check_unit(self.h, layer, unit))
+
+    def residency(self, cap):
+        out = (abi.ss_dg_unit * cap)()
+        total = C.c_uint32()
+        abi.check(abi.load().ss_dg_residency(self.h, out, cap, C.byref(total)))
+        return [(out[i].gated, out[i].unit) for i in range(min(cap, total.value))], total.value
+
+    def reset_open(self):
+        abi.check(abi.load().ss_dg_reset_open(self.h))
+
+
+class TokenGraph:
+    """One decode step captured once (libtsb_engine.so): begin, per layer export / wait / reader, end."""
+
+    def __init__(self, ctx, n_gated, ids_dev, n_ids, out_dev, stream, slices=64, mode=0, pred_dev=0, n_pred=0,
+                 with_reader=True):
+        eng = abi.load_engine()
+        self.exec = C.c_void_p()
+        self.stream = stream
+        rc = eng.tse_capture_token(ctx.h, n_gated, ids_dev, n_ids, pred_dev or None, n_pred, out_dev, slices, mode,
+                                   1 if with_reader else 0, stream, C.byref(self.exec))
+        if rc != 0:
+            msg = abi.load().ss_last_error().decode(errors="replace") if rc >= 1000 else ""
+            raise RuntimeError("tse_capture_token failed: %d %s" % (rc, msg))
+
+    def launch(self):
+        rc = abi.load_engine().tse_launch(self.exec, self.stream)
+        if rc != 0:
+            raise RuntimeError("cudaGraphLaunch failed: %d" % rc)
+
+    def close(self):
+        if self.exec:
+            abi.load_engine().tse_destroy(self.exec)
+            self.exec = C.c_void_p()
+
+    def __del__(self):
+        self.close()
+
+
+def replay_config(n_units, part_bytes, persistent_slots, bank_slots, blocks, spare_target, order, tokens, n_ids,
+                  n_pred=0, prefetch_reserve=0xFFFFFFFF, prefetch_per_layer=4, prefetch_per_token=48, wb_defer=1,
+                  wb_on_d2h=1, wb_layer_bytes=0, wb_max_outstanding=0, move_bytes=0):
+    """A dg_replay_config with its arrays kept alive on the returned object."""
+    c = abi.dg_replay_config()
+    keep = {}
+    keep["n_units"] = (C.c_uint32 * len(n_units))(*n_units)
+    keep["part_bytes"] = (C.c_uint64 * len(part_bytes))(*part_bytes)
+    keep["order"] = (C.c_uint32 * max(1, len(order)))(*order)
+    c.n_gated = len(n_units)
+    c.n_units = keep["n_units"]
+    c.n_parts = len(part_bytes)
+    c.part_bytes = keep["part_bytes"]
+    c.persistent_slots, c.bank_slots, c.blocks, c.spare_target = persistent_slots, bank_slots, blocks, spare_target
+    c.prefetch_reserve, c.prefetch_per_layer, c.prefetch_per_token = prefetch_reserve, prefetch_per_layer, \
+        prefetch_per_token
+    c.wb_defer, c.wb_on_d2h, c.wb_layer_bytes, c.wb_max_outstanding = wb_defer, wb_on_d2h, wb_layer_bytes, \
+        wb_max_outstanding
+    c.n_order = len(order)
+    c.order = keep["order"]
+    c.tokens, c.n_ids, c.n_pred, c.move_bytes = tokens, n_ids, n_pred, move_bytes
+    c._keep = keep
+    return c
+
+
+def replay(cfg, ids, preds=None, src_units=None, want_reads=False):
+    """This library's deterministic replay (tsb_test_dg_replay): (tables, stats[, read_sum])."""
+    keys = sum(cfg.n_units[i] for i in range(cfg.n_gated))
+    ids = np.ascontiguousarray(ids, dtype=np.int32)
+    tables = np.empty((cfg.tokens, keys), dtype=np.int32)
+    stats = np.empty((cfg.tokens, 16), dtype=np.uint64)
+    reads = np.zeros((cfg.tokens, cfg.n_gated, cfg.n_ids), dtype=np.uint64) if want_reads else None
+    p = np.ascontiguousarray(preds, dtype=np.int32) if preds is not None else None
+    P = C.POINTER
+    abi.check(abi.load().tsb_test_dg_replay(
+        C.byref(cfg), ids.ctypes.data_as(P(C.c_int32)), p.ctypes.data_as(P(C.c_int32)) if p is not None else None,
+        tables.ctypes.data_as(P(C.c_int32)), stats.ctypes.data_as(P(C.c_uint64)),
+        src_units.ctypes.data_as(P(C.c_uint8)) if src_units is not None else None,
+        reads.ctypes.data_as(P(C.c_uint64)) if reads is not None else None))
+    return (tables, stats, reads) if want_reads else (tables, stats)
