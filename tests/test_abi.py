@@ -1,0 +1,76 @@
+"""The drop-in boundary: libtierstream.so exports every function include/*.h declares (ss_*, ts_*, ss_test_*, tsb_*),
+and every versioned struct has the reference header's size and field offsets (tests/golden/abi_layout.json, generated
+from the reference's include/strix_stream/ss.h by tests/golden/gen_abi_layout.py)."""
+import json
+import os
+import re
+import subprocess
+import tempfile
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADERS = ["include/strix_stream/ss.h", "include/strix_stream/ss_test.h", "include/tierstream/ts.h",
+           "include/tierstream/tsb.h"]
+
+
+def declared():
+    names = set()
+    for h in HEADERS:
+        text = re.sub(r"/\*.*?\*/", " ", open(os.path.join(ROOT, h)).read(), flags=re.S)
+        for m in re.finditer(r"(?:SS|TS)_API\s+[^;(]*?\b((?:ss|ts|tsb)_\w+)\s*\(", text):
+            names.add(m.group(1))
+    return names
+
+
+def exported():
+    out = subprocess.run(["nm", "-D", "--defined-only", os.path.join(ROOT, "tierstream_b200", "libtierstream.so")],
+                         capture_output=True, text=True, check=True).stdout
+    return {line.split()[-1] for line in out.splitlines() if line.strip()}
+
+
+def test_every_declared_function_is_exported():
+    d, e = declared(), exported()
+    assert len(d) > 300
+    missing = sorted(d - e)
+    assert not missing, "declared but not exported: %s" % missing
+
+
+def test_ts_names_pair_with_ss_names():
+    d = declared()
+    for n in d:
+        if n.startswith("ts_"):
+            assert "ss_" + n[3:] in d
+
+
+def test_library_loads_and_reports(lib):
+    assert lib.ss_abi_version() == 1
+    assert lib.tsb_cuda_arch() == 100
+
+
+def _layout_with(include_dir):
+    golden = json.load(open(os.path.join(ROOT, "tests", "golden", "abi_layout.json")))
+    src = ['#include <stdio.h>', '#include <stddef.h>', '#include "strix_stream/ss.h"', "int main(void) {"]
+    for struct, fields in golden.items():
+        src.append('printf("%s __sizeof__ %%zu\\n", sizeof(%s));' % (struct, struct))
+        for f in fields["fields"]:
+            src.append('printf("%s %s %%zu\\n", offsetof(%s, %s));' % (struct, f, struct, f))
+    src.append("return 0; }")
+    with tempfile.TemporaryDirectory() as d:
+        c = os.path.join(d, "l.c")
+        open(c, "w").write("\n".join(src))
+        subprocess.run(["gcc", "-std=c11", "-I", include_dir, c, "-o", os.path.join(d, "l")], check=True)
+        out = subprocess.run([os.path.join(d, "l")], capture_output=True, text=True, check=True).stdout
+    got = {}
+    for line in out.splitlines():
+        s, f, v = line.split()
+        got.setdefault(s, {})[f] = int(v)
+    return golden, got
+
+
+def test_struct_layouts_match_reference_header():
+    golden, got = _layout_with(os.path.join(ROOT, "include"))
+    for struct, g in golden.items():
+        assert got[struct]["__sizeof__"] == g["size"], struct
+        for f, off in g["fields"].items():
+            assert got[struct][f] == off, "%s.%s" % (struct, f)

@@ -1,0 +1,138 @@
+"""Device-gated decode on the GPU through the C ABI: every routed unit's bytes read by the engine's kernels equal the
+source bytes (the oracle's checksum of the model file), the slot table after every token equals the reference
+DgCore's on the same trace (deterministic schedule), and the failure paths end the token with an error instead of a
+hang."""
+import os
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+import oracle  # noqa: E402
+from tierstream_b200 import abi, harness, runtime, synth  # noqa: E402
+
+
+def expected_sums(model, orc):
+    """oracle checksum of every unit, layer-major."""
+    out = np.zeros(model.layers * model.units, dtype=np.uint64)
+    buf = np.empty(model.unit_bytes, dtype=np.uint8)
+    for L in range(model.layers):
+        for u in range(model.units):
+            orc.orc_fill_bytes(model.seed, model.unit_offset(L, u), model.unit_bytes, buf.ctypes.data)
+            out[L * model.units + u] = orc.orc_checksum(buf.ctypes.data, model.unit_bytes)
+    return out
+
+
+@pytest.fixture(scope="module")
+def small_model():
+    m = synth.Model(os.path.join(harness.model_dir(), "tsb-test-small.bin"), layers=6, units=16,
+                    part_bytes=(2048, 2048, 4096), seed=3, top_k=2, with_hash=True, base=0)
+    m.write()
+    return m
+
+
+def run_tokens(run, ids, want, preds=None):
+    for t in range(ids.shape[0]):
+        got = run.step(ids[t], preds[t] if preds is not None else None)
+        keys = np.arange(run.G)[:, None] * run.U + ids[t]
+        assert np.array_equal(got, want[keys]), "token %d read wrong bytes" % t
+
+
+def replay_cfg_for(run, model, ids):
+    P = model.layers * model.units - len(run.resident_keys)
+    return runtime.replay_config([model.units] * model.layers, list(model.part_bytes),
+                                 persistent_slots=len(run.resident_keys) + model.layers, bank_slots=run.n_ids,
+                                 blocks=P + model.layers, spare_target=model.layers, order=run.resident_keys,
+                                 tokens=ids.shape[0], n_ids=run.n_ids)
+
+
+@pytest.mark.parametrize("copy_mode", ["kernel", "ce"])
+def test_bytes_and_tables_match_reference(small_model, orc, ref, monkeypatch, copy_mode):
+    monkeypatch.setenv("TSB_DG_DETERMINISTIC", "1")
+    monkeypatch.setenv("TSB_COPY_MODE", copy_mode)
+    m = small_model
+    ids = synth.zipf_trace(40, m.layers, m.units, 2, s=1.1, seed=11)
+    run = harness.DgRun(m, residents_per_layer=3, max_ids=2, verify=True)
+    try:
+        want = expected_sums(m, orc)
+        t_ref, s_ref = oracle.ref_replay(replay_cfg_for(run, m, ids), ids)
+        for t in range(ids.shape[0]):
+            got = run.step(ids[t])
+            keys = np.arange(m.layers)[:, None] * m.units + ids[t]
+            assert np.array_equal(got, want[keys]), "token %d read wrong bytes" % t
+            assert np.array_equal(run.ctx.table(run.keys), t_ref[t]), "slot table differs after token %d" % t
+        st = run.ctx.stats()
+        assert st["misses"] == s_ref[-1][2] and st["fetched"] == s_ref[-1][4] and st["evicted"] == s_ref[-1][10]
+        assert st["misses"] > 20
+        run.ctx.check()
+        for L in range(m.layers):
+            for u in range(m.units):
+                run.ctx.check_unit(L, u)
+    finally:
+        run.close()
+
+
+def test_predictions_and_boundary_writebacks(small_model, orc):
+    m = small_model
+    ids = synth.zipf_trace(30, m.layers, m.units, 2, s=0.9, seed=5)
+    preds = synth.zipf_trace(30, m.layers, m.units, 2, s=0.9, seed=6)
+    run = harness.DgRun(m, residents_per_layer=2, spare_per_layer=2, max_ids=2, n_pred=2, wb_defer=0)
+    try:
+        run_tokens(run, ids, expected_sums(m, orc), preds)
+        st = run.ctx.stats()
+        assert st["prefetched"] > 0 and st["writebacks_done"] > 0
+        run.ctx.check()
+    finally:
+        run.close()
+
+
+def test_reset_open_restores_placement(small_model, orc, monkeypatch):
+    monkeypatch.setenv("TSB_DG_DETERMINISTIC", "1")
+    m = small_model
+    run = harness.DgRun(m, residents_per_layer=3, max_ids=2)
+    try:
+        open_table = run.ctx.table(run.keys).copy()
+        want = expected_sums(m, orc)
+        run_tokens(run, synth.zipf_trace(25, m.layers, m.units, 2, s=0.5, seed=9), want)
+        assert not np.array_equal(run.ctx.table(run.keys), open_table)
+        run.ctx.reset_open()
+        assert np.array_equal(run.ctx.table(run.keys), open_table)
+        run.ctx.check()
+        for L in range(m.layers):
+            for u in range(m.units):
+                run.ctx.check_unit(L, u)
+        run_tokens(run, synth.zipf_trace(5, m.layers, m.units, 2, s=0.5, seed=10), want)
+    finally:
+        run.close()
+
+
+def test_bad_id_fails_the_token(small_model):
+    m = small_model
+    run = harness.DgRun(m, residents_per_layer=3, max_ids=2, timeout_ms=2000)
+    try:
+        ids = synth.zipf_trace(1, m.layers, m.units, 2, seed=1)[0].copy()
+        ids[2, 1] = m.units + 3
+        with pytest.raises(abi.TsError) as e:
+            run.step(ids)
+        assert e.value.status == abi.SS_E_BACKEND and "out of range" in str(e.value)
+        with pytest.raises(abi.TsError):  # poisoned
+            run.ctx.begin()
+    finally:
+        run.close()
+
+
+def test_stopped_service_times_out_on_the_device(small_model):
+    """The wait kernel's bounded wait: nothing publishes ready, so it gives up after dg_wait_timeout_ms and the token
+    fails on the host; no GPU fault or hang is involved."""
+    m = small_model
+    run = harness.DgRun(m, residents_per_layer=1, max_ids=2, timeout_ms=300)
+    try:
+        abi.check(abi.load().ss_test_dg_stop_service(run.ctx.h))
+        ids = synth.zipf_trace(1, m.layers, m.units, 2, seed=2)[0]
+        with pytest.raises(abi.TsError) as e:
+            run.step(ids)
+        assert e.value.status == abi.SS_E_BACKEND
+    finally:
+        run.close()

@@ -1,0 +1,128 @@
+"""The data-path kernels through the C ABI (tsb_land, tsb_xxh64_units) against the oracle: land copies are byte
+exact in every direction and alignment, their entries and ready word are published, and the device xxh64 equals the
+reference's host xxh64 bit for bit."""
+import ctypes as C
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+from tierstream_b200 import abi  # noqa: E402
+
+P = C.POINTER
+
+
+def land(srcs, dsts, sizes, stream, slot_of=None, keys=(), vals=(), ready=None, ready_val=0, counter=None, blocks=0):
+    n = len(srcs)
+    s = (C.c_void_p * max(n, 1))(*srcs)
+    d = (C.c_void_p * max(n, 1))(*dsts)
+    b = (C.c_uint64 * max(n, 1))(*sizes)
+    k = (C.c_uint32 * max(len(keys), 1))(*keys)
+    v = (C.c_int32 * max(len(vals), 1))(*vals)
+    abi.check(abi.load().tsb_land(s, d, b, n, slot_of, k, v, len(keys), ready, ready_val, counter, blocks, stream))
+
+
+def test_land_host_to_device_any_alignment():
+    rng = np.random.default_rng(1)
+    host = torch.from_numpy(rng.integers(0, 256, size=8 << 20, dtype=np.uint8)).pin_memory()
+    dev = torch.zeros(8 << 20, dtype=torch.uint8, device="cuda")
+    s = torch.cuda.Stream()
+    # copies of assorted sizes and offsets, disjoint destinations
+    plan, pos = [], 0
+    for size in [1, 15, 16, 17, 255, 4096, 65535, 65536, 65537, 1 << 20, 3 * 1000 + 7, 2 << 20]:
+        src_off = int(rng.integers(0, 64))
+        plan.append((src_off + pos, pos + int(rng.integers(0, 32)), size))
+        pos += size + 64
+    land([host.data_ptr() + a for a, _, _ in plan], [dev.data_ptr() + b for _, b, _ in plan], [n for *_, n in plan],
+         s.cuda_stream)
+    s.synchronize()
+    h, d = host.numpy(), dev.cpu().numpy()
+    for a, b, n in plan:
+        assert np.array_equal(d[b:b + n], h[a:a + n]), (a, b, n)
+
+
+def test_land_publishes_entries_and_ready_after_copies():
+    rng = np.random.default_rng(2)
+    n_units, unit = 24, 3 << 20
+    host = torch.from_numpy(rng.integers(0, 256, size=n_units * unit, dtype=np.uint8)).pin_memory()
+    dev = torch.zeros(n_units * unit, dtype=torch.uint8, device="cuda")
+    slot_of = torch.full((64,), -1, dtype=torch.int32, device="cuda")
+    words = torch.zeros(4, dtype=torch.int32, device="cuda")  # [0] counter, [1] ready
+    s = torch.cuda.Stream()
+    order = rng.permutation(n_units)
+    land([host.data_ptr() + int(u) * unit for u in order], [dev.data_ptr() + i * unit for i in range(n_units)],
+         [unit] * n_units, s.cuda_stream, slot_of=slot_of.data_ptr(), keys=[int(u) for u in order],
+         vals=list(range(n_units)), ready=words.data_ptr() + 4, ready_val=77, counter=words.data_ptr())
+    s.synchronize()
+    so = slot_of.cpu().numpy()
+    for i, u in enumerate(order):
+        assert so[u] == i
+    assert words[1].item() == 77 and words[0].item() == 0  # ready published, counter re-zeroed
+    assert np.array_equal(dev.cpu().numpy(), host.numpy().reshape(n_units, unit)[order].reshape(-1))
+
+
+def test_land_device_to_host_and_device_to_device():
+    rng = np.random.default_rng(3)
+    src = torch.from_numpy(rng.integers(0, 256, size=4 << 20, dtype=np.uint8)).cuda()
+    host = torch.zeros(4 << 20, dtype=torch.uint8).pin_memory()
+    dev2 = torch.zeros(4 << 20, dtype=torch.uint8, device="cuda")
+    s = torch.cuda.Stream()
+    half = 2 << 20
+    land([src.data_ptr(), src.data_ptr() + half], [host.data_ptr(), dev2.data_ptr() + half], [half, half],
+         s.cuda_stream, blocks=7)
+    s.synchronize()
+    a = src.cpu().numpy()
+    assert np.array_equal(host.numpy()[:half], a[:half])
+    assert np.array_equal(dev2.cpu().numpy()[half:], a[half:])
+
+
+def xxh_units(units, expect=None):
+    """units: list of lists of (device ptr, bytes). Returns (hashes, mismatches)."""
+    lib = abi.load()
+    n = len(units)
+    spans = (C.c_void_p * (4 * n))()
+    sb = (C.c_uint64 * (4 * n))()
+    ns = (C.c_uint32 * n)()
+    for i, u in enumerate(units):
+        ns[i] = len(u)
+        for j, (p, b) in enumerate(u):
+            spans[4 * i + j] = p
+            sb[4 * i + j] = b
+    scratch = torch.zeros(n * 72 // 8 + 1, dtype=torch.int64, device="cuda")
+    out = torch.zeros(n, dtype=torch.int64, device="cuda")
+    mism = torch.zeros(1, dtype=torch.int32, device="cuda")
+    exp = torch.tensor(np.array(expect, dtype=np.uint64).view(np.int64), device="cuda") if expect else None
+    s = torch.cuda.Stream()
+    abi.check(lib.tsb_xxh64_units(spans, sb, ns, n, scratch.data_ptr(), exp.data_ptr() if exp is not None else None,
+                                  out.data_ptr(), mism.data_ptr() if exp is not None else None, s.cuda_stream))
+    return out.cpu().numpy().view(np.uint64), int(mism.item())
+
+
+def test_device_xxh64_matches_oracle(orc):
+    rng = np.random.default_rng(4)
+    data = torch.from_numpy(rng.integers(0, 256, size=16 << 20, dtype=np.uint8)).cuda()
+    h = data.cpu().numpy()
+    base = data.data_ptr()
+    units, want, pos = [], [], 0
+    # one-span units of every tail length, multi-span units (32-byte multiples but the last), odd spans (one-lane path)
+    layouts = [[n] for n in [0, 1, 5, 8, 31, 32, 33, 64, 100, 1024, 1025, 4096 + 17, 65536, 1 << 20, (3 << 20) + 3]]
+    layouts += [[2048, 2048, 4096], [256, 512, 256, 1000], [32, 32], [4096, 9]]
+    layouts += [[1000, 24], [3, 5, 7], [33, 64]]
+    for spans in layouts:
+        u, blob = [], []
+        for b in spans:
+            pos = (pos + 255) // 256 * 256
+            u.append((base + pos, b))
+            blob.append(h[pos:pos + b])
+            pos += b
+        units.append(u)
+        cat = np.concatenate(blob) if blob else np.zeros(0, dtype=np.uint8)
+        want.append(orc.orc_xxh64(cat.ctypes.data, cat.size, 0))
+    got, _ = xxh_units(units)
+    assert [int(x) for x in got] == want
+    bad = list(want)
+    bad[3] ^= 1
+    _, mism = xxh_units(units, expect=bad)
+    assert mism == 1

@@ -1,0 +1,98 @@
+"""Drives a device-gated context the way an engine does (tests, smoke and bench.py): a synthetic model on disk, its
+descriptor and plan, ss_open, then per token ss_begin / one captured graph (begin, per layer export -> wait -> reader,
+end) / ss_end, with the token's routed ids copied from pinned host memory into the device buffer the graph reads.
+Everything that moves a byte is the library (libtierstream.so); torch only provides device memory and streams.
+"""
+import ctypes as C
+import os
+
+import numpy as np
+import torch
+
+from . import abi, runtime, synth
+
+
+class DgRun:
+    def __init__(self, model, residents_per_layer=None, resident_keys=None, spare_per_layer=1, max_ids=2,
+                 host_spare_units=None, diag=False, test_hooks=True, wb_defer=1, wb_stream=1, verify=False,
+                 n_pred=0, slices=64, mode=0, timeout_ms=10000, device_bytes=None, with_reader=True,
+                 resident_order=None):
+        self.model = model
+        G, U = model.layers, model.units
+        self.G, self.U, self.n_ids, self.n_pred = G, U, max_ids, n_pred
+        tiers = [abi.SS_TIER_PINNED] * (G * U)
+        if resident_keys is None:
+            resident_keys = []
+            for g in range(G):
+                order = resident_order[g] if resident_order else list(range(U))
+                resident_keys += [g * U + e for e in order[:residents_per_layer]]
+        for k in resident_keys:
+            tiers[k] = abi.SS_TIER_RESIDENT
+        self.resident_keys = list(resident_keys)
+        b = abi.budget_defaults()
+        unit = model.unit_bytes
+        slots = len(resident_keys) + spare_per_layer * G + 2 * max_ids + 1
+        b.device_bytes = device_bytes or (slots * unit + (4 << 30))
+        b.margin_gib = 1.0 / 1024
+        b.margin_fraction = 0.0
+        b.tier_mode = abi.SS_TIER_MODE_EXCLUSIVE
+        b.dynamic_slots_per_layer = spare_per_layer
+        b.ring_slots = 2 * max_ids + 1
+        b.host_spare_units = host_spare_units if host_spare_units is not None else spare_per_layer * G
+        hs = (unit + 4095) // 4096 * 4096
+        b.host_pinned_bytes = (G * U - len(resident_keys) + b.host_spare_units + 2) * hs + (64 << 20)
+        self.desc = runtime.Desc(model.desc())
+        self.plan = runtime.Plan(self.desc, b, tiers=tiers)
+        o = abi.options_defaults()
+        o.forward_mode = abi.SS_FORWARD_DEVICE_GATED
+        o.pin_planned = 0
+        o.dg_max_ids = max_ids
+        o.dg_test_hooks = 1 if test_hooks else 0
+        o.dg_diag = 1 if diag else 0
+        o.dg_wb_defer = wb_defer
+        o.dg_wb_stream = wb_stream
+        o.verify_hash = 1 if verify else 0
+        o.dg_wait_timeout_ms = timeout_ms
+        self.ctx = runtime.DgContext(self.desc, self.plan, o)
+        self.stream = torch.cuda.Stream()
+        self.ids_pin = torch.zeros(G * max_ids, dtype=torch.int32).pin_memory()
+        self.ids_dev = torch.zeros(G * max_ids, dtype=torch.int32, device="cuda")
+        self.pred_pin = torch.zeros(max(1, G * n_pred), dtype=torch.int32).pin_memory()
+        self.pred_dev = torch.zeros(max(1, G * n_pred), dtype=torch.int32, device="cuda")
+        self.out_dev = torch.zeros(G * max_ids, dtype=torch.int64, device="cuda")
+        self.out_pin = torch.zeros(G * max_ids, dtype=torch.int64).pin_memory()
+        self.graph = runtime.TokenGraph(self.ctx, G, self.ids_dev.data_ptr(), max_ids, self.out_dev.data_ptr(),
+                                        self.stream.cuda_stream, slices=slices, mode=mode,
+                                        pred_dev=self.pred_dev.data_ptr() if n_pred else 0, n_pred=n_pred,
+                                        with_reader=with_reader)
+        self.keys = G * U
+
+    def step(self, ids, preds=None, sync=True):
+        """One token: routed ids [G][max_ids] (and predictions [G][n_pred]); returns the readers' checksums."""
+        self.ids_pin.numpy()[:] = np.asarray(ids, dtype=np.int32).reshape(-1)
+        if preds is not None:
+            self.pred_pin.numpy()[:self.G * self.n_pred] = np.asarray(preds, dtype=np.int32).reshape(-1)
+        self.ctx.begin()
+        with torch.cuda.stream(self.stream):
+            self.ids_dev.copy_(self.ids_pin, non_blocking=True)
+            if preds is not None:
+                self.pred_dev.copy_(self.pred_pin, non_blocking=True)
+            self.graph.launch()
+            self.out_pin.copy_(self.out_dev, non_blocking=True)
+        if sync:
+            self.stream.synchronize()
+        self.ctx.end()
+        return self.out_pin.numpy().reshape(self.G, self.n_ids).astype(np.uint64)
+
+    def close(self):
+        if getattr(self, "graph", None):
+            self.graph.close()
+        if getattr(self, "ctx", None):
+            self.ctx.close()
+
+
+def model_dir():
+    for d in ("/dev/shm", "/tmp"):
+        if os.path.isdir(d) and os.access(d, os.W_OK):
+            return d
+    return "."
