@@ -1,0 +1,307 @@
+"""Benchmark: the expert-miss stream of device-gated decode (Mixtral-8x7B-shaped MoE on one B200).
+
+Workload "mixtral-8x7b-dg": 32 MoE layers x 8 experts, each expert three parts (gate / up / down) of 33,030,144 bytes
+(14336 x 4096 x 4.5 bits), random bytes (the synthetic generator, seeded); VRAM budget 40 % of the experts (102
+residents, the most popular by layer, +1 spare slot per layer, 2 banks of 2 + the guard), the rest in pinned RAM,
+exclusive tiers; batch-1 decode with top-2 Zipf(1.1) routes, one token = one step: ss_begin, the captured graph
+(begin; per layer export -> wait -> the engine's reader of the two routed experts; end), ss_end.
+
+Printed metric: expert-miss stream GB/s = bytes landed by the miss service (demand + prefetch copies) per second of
+decode, aggregated over ranks (N > 1 runs N independent replicas, "replicas only": the config fits one GPU).
+`value` is device time (CUDA events on the engine stream) with the routed ids already in HBM; `e2e` is the same steps
+through the public ABI with the ids copied from pinned host memory and the readers' results copied back each step,
+timed by the host clock. `--impl reference` times the reference's own DgCore (compiled from its sources) with a host
+memcpy transport on the host cores, the same trace and metric.
+"""
+import argparse
+import ctypes as C
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+LAYERS, UNITS, PART = 32, 8, 33030144
+TOP_K, ZIPF, RESIDENTS, SPARE = 2, 1.1, 102, 1
+METRIC = "expert-miss stream GB/s (device-gated decode, Mixtral-8x7B-shaped MoE)"
+
+
+def args_():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=64)
+    p.add_argument("--warmup", type=int, default=8)
+    p.add_argument("--impl", default="tierstream", choices=["tierstream", "reference"])
+    p.add_argument("--copy-mode", default=os.environ.get("TSB_COPY_MODE", "auto"), choices=["auto", "kernel", "ce"])
+    p.add_argument("--wb-defer", type=int, default=1, help="ss_options.dg_wb_defer (the reference default 1)")
+    p.add_argument("--wb-stream", type=int, default=1, help="ss_options.dg_wb_stream (the reference default 1)")
+    p.add_argument("--spare", type=int, default=SPARE, help="spare slots per layer (dynamic_slots_per_layer)")
+    p.add_argument("--cpu-sample-tokens", type=int, default=6)
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    return p.parse_args()
+
+
+def resident_keys(seed):
+    from tierstream_b200 import synth
+    pop = synth.popularity_order(LAYERS, UNITS, s=ZIPF, seed=seed)
+    per = [RESIDENTS // LAYERS + (1 if g < RESIDENTS % LAYERS else 0) for g in range(LAYERS)]
+    return [g * UNITS + e for g in range(LAYERS) for e in pop[g][:per[g]]]
+
+
+def model_path():
+    from tierstream_b200 import harness
+    return os.path.join(harness.model_dir(), "tsb-bench-mixtral-dg.bin")
+
+
+class Clocks:
+    """nvidia-smi samples during the timed region (clocks and throttle reasons)."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", "--query-gpu=" + self.Q, "--format=csv,noheader,nounits",
+                                       "-lms", "200"], stdout=self.f, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.p = None
+
+    def stop(self):
+        if self.p:
+            self.p.terminate()
+            try:
+                self.p.wait(5)
+            except subprocess.TimeoutExpired:
+                self.p.kill()
+        self.f.seek(0)
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.f.read().splitlines():
+            c = [x.strip() for x in line.split(",")]
+            if len(c) < 9 or c[0] != str(self.index):
+                continue
+            try:
+                sm.append(float(c[1]))
+                mx = float(c[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, c[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        os.unlink(self.f.name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def h2d_peak(torch):
+    """Best-of-5 copy-engine pinned -> HBM bandwidth of 1 GiB (the host-link denominator; MEASURED_PEAKS.json has no
+    host-link figure)."""
+    n = 1 << 30
+    h = torch.empty(n, dtype=torch.uint8).pin_memory()
+    d = torch.empty(n, dtype=torch.uint8, device="cuda")
+    s = torch.cuda.Stream()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    best = None
+    with torch.cuda.stream(s):
+        for i in range(6):
+            a.record(s)
+            d.copy_(h, non_blocking=True)
+            b.record(s)
+            b.synchronize()
+            if i:
+                ms = a.elapsed_time(b)
+                best = ms if best is None else min(best, ms)
+    del h, d
+    return n / (best / 1e3) / 1e9
+
+
+def reference_sample(ids, tokens):
+    """The reference DgCore + memcpy transport on `tokens` tokens of the trace (oracle/_ref): (miss bytes, seconds)."""
+    import oracle
+    from tierstream_b200 import runtime
+    keys = resident_keys(1)
+    P = LAYERS * UNITS - len(keys)
+    cfg = runtime.replay_config([UNITS] * LAYERS, [PART] * 3, persistent_slots=len(keys) + SPARE * LAYERS,
+                                bank_slots=TOP_K, blocks=P + SPARE * LAYERS, spare_target=SPARE * LAYERS,
+                                order=keys, tokens=tokens, n_ids=TOP_K, move_bytes=2)
+    t0 = time.perf_counter()
+    _, stats = oracle.ref_replay(cfg, ids[:tokens])
+    dt = time.perf_counter() - t0
+    moved = int(stats[-1][4] + stats[-1][5]) * 3 * PART  # fetched + prefetched units
+    return moved, dt
+
+
+def run_reference(a):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    from tierstream_b200 import synth
+    ids = synth.zipf_trace(a.warmup + a.steps, LAYERS, UNITS, TOP_K, s=ZIPF, seed=1)
+    import oracle
+    if not oracle.ref_available():
+        print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libtsref.so (the reference's sources "
+                                                              "compiled by oracle/Makefile) is not built"}))
+        return 0
+    moved, dt = reference_sample(ids, a.warmup + a.steps)
+    # the replay cannot split warm-up from timed tokens inside one call: time both and subtract the warm-up alone
+    w_moved, w_dt = reference_sample(ids, a.warmup) if a.warmup else (0, 0.0)
+    moved, dt = moved - w_moved, max(dt - w_dt, 1e-9)
+    v = moved / dt / 1e9
+    line = {"impl": "reference", "metric": METRIC, "value": round(v, 3), "unit": "GB/s", "n_gpus": a.gpus,
+            "steps": a.steps, "warmup": a.warmup, "ms_per_step": round(dt * 1e3 / a.steps, 3),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u8", "data": "synthetic",
+            "config": {"workload": "mixtral-8x7b-dg", "layers": LAYERS, "experts": UNITS, "part_bytes": PART,
+                       "top_k": TOP_K, "zipf": ZIPF, "residents": RESIDENTS, "tokens": a.steps},
+            "cpu_baseline": {"value": round(v, 3), "unit": "GB/s", "cores": 1, "kind": "reference",
+                             "sample": "%d tokens of the trace through the reference DgCore (oracle/_ref) with a "
+                                       "host memcpy transport (every copy moves its bytes; slots alias 4 buffers)"
+                                       % a.steps},
+            "e2e": {"value": round(v, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line))
+    return 0
+
+
+def main():
+    a = args_()
+    if a.impl == "reference":
+        return run_reference(a)
+    os.environ["TSB_COPY_MODE"] = a.copy_mode
+    import torch
+    from tierstream_b200 import abi, harness, synth
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600))
+
+    def barrier():
+        if dist:
+            dist.barrier()
+
+    model = synth.Model(model_path(), LAYERS, UNITS, [PART] * 3, seed=0, top_k=TOP_K)
+    if rank == 0:
+        model.write()
+    barrier()
+    peak = h2d_peak(torch) if rank == 0 else None
+    ids = synth.zipf_trace(a.warmup + a.steps, LAYERS, UNITS, TOP_K, s=ZIPF, seed=1 + rank)
+    t_open = time.perf_counter()
+    run = harness.DgRun(model, resident_keys=resident_keys(1 + rank), spare_per_layer=a.spare, max_ids=TOP_K,
+                        diag=True, test_hooks=False, mode=1, slices=128, wb_defer=a.wb_defer, wb_stream=a.wb_stream)
+    t_open = time.perf_counter() - t_open
+    unit = model.unit_bytes
+    try:
+        for t in range(a.warmup):
+            run.step(ids[t])
+        # (1) device-timed: ids already in HBM (the whole trace resident), one D2D copy per step into the graph's
+        # input buffer, no host copy
+        trace_dev = torch.from_numpy(ids[a.warmup:].reshape(a.steps, -1).copy()).cuda()
+        s0 = run.ctx.stats()
+        j0 = json.loads(run.ctx.stats_json())["dg"]
+        clocks = Clocks(local)
+        barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(run.stream)
+        for t in range(a.steps):
+            run.ctx.begin()
+            with torch.cuda.stream(run.stream):
+                run.ids_dev.copy_(trace_dev[t], non_blocking=True)
+                run.graph.launch()
+            run.ctx.end()
+        e1.record(run.stream)
+        e1.synchronize()
+        barrier()
+        clk = clocks.stop()
+        dev_ms = e0.elapsed_time(e1)
+        s1 = run.ctx.stats()
+        j1 = json.loads(run.ctx.stats_json())["dg"]
+        units_moved = (s1["fetched"] - s0["fetched"]) + (s1["prefetched"] - s0["prefetched"])
+        moved = units_moved * unit
+        dma_ms = j1["dma_ms_total"] - j0["dma_ms_total"]
+        land_launches = j1["land_launches"] - j0["land_launches"]
+        # (2) end to end: the same steps of a second trace window through the ABI with host buffers
+        ids2 = synth.zipf_trace(a.steps, LAYERS, UNITS, TOP_K, s=ZIPF, seed=101 + rank)
+        s2 = run.ctx.stats()
+        barrier()
+        w0 = time.perf_counter()
+        for t in range(a.steps):
+            run.step(ids2[t])
+        w1 = time.perf_counter()
+        barrier()
+        s3 = run.ctx.stats()
+        moved_e2e = ((s3["fetched"] - s2["fetched"]) + (s3["prefetched"] - s2["prefetched"])) * unit
+        e2e_s = w1 - w0
+        misses = s1["misses"] - s0["misses"]
+        lookups = s1["lookups"] - s0["lookups"]
+        dg = {k: s1[k] - s0[k] for k in ("fetched", "prefetched", "bank_serves", "evicted", "evict_short",
+                                         "writebacks_done", "collected_mid", "wb_forced", "wb_forced_wait_ns",
+                                         "wb_boundary_flushed", "wb_deferred", "wb_cancelled", "resurrected",
+                                         "wb_issued_bytes", "covered")}
+    finally:
+        run.close()
+
+    tot = torch.tensor([moved, moved_e2e, dev_ms, e2e_s, dma_ms], dtype=torch.float64, device="cuda")
+    if dist:
+        s = tot[[0, 1]].clone()
+        m = tot[[2, 3, 4]].clone()
+        dist.all_reduce(s, op=dist.ReduceOp.SUM)
+        dist.all_reduce(m, op=dist.ReduceOp.MAX)
+        tot = torch.cat([s, m])
+    moved_all, moved_e2e_all, dev_ms_max, e2e_s_max, dma_ms_max = [float(x) for x in tot.cpu()]
+    if rank != 0:
+        if dist:
+            dist.destroy_process_group()
+        return 0
+    value = moved_all / (dev_ms_max / 1e3) / 1e9
+    e2e = moved_e2e_all / e2e_s_max / 1e9
+    achieved = (moved / (dma_ms / 1e3) / 1e9) if dma_ms > 0 else None
+    line = {
+        "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": world, "steps": a.steps,
+        "warmup": a.warmup, "ms_per_step": round(dev_ms_max / a.steps, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "u8", "data": "synthetic (seeded random bytes and Zipf routes)",
+        "config": {"workload": "mixtral-8x7b-dg", "layers": LAYERS, "experts": UNITS, "part_bytes": PART,
+                   "unit_bytes": unit, "top_k": TOP_K, "zipf": ZIPF, "residents": RESIDENTS,
+                   "spare_slots_per_layer": SPARE, "parallelism": "replicas" if world > 1 else "single",
+                   "copy_mode": a.copy_mode, "l2": "inputs larger than L2 (99 MB units, 10 GB arena)"},
+        "tokens_per_s": round(a.steps * world / (dev_ms_max / 1e3), 3),
+        "misses_per_token": round(misses / a.steps, 3), "lookups_per_token": round(lookups / a.steps, 3),
+        "e2e": {"value": round(e2e, 3), "unit": "GB/s", "h2d_bytes_per_step": LAYERS * TOP_K * 4,
+                "d2h_bytes_per_step": LAYERS * TOP_K * 8,
+                "tokens_per_s": round(a.steps * world / e2e_s_max, 3)},
+        "roofline": {"bound": "link", "kernel": "miss service (demand copies + entries + ready on the demand stream)",
+                     "achieved": round(achieved, 3) if achieved else None, "peak": round(peak, 3), "unit": "GB/s",
+                     "frac": round(achieved / peak, 4) if achieved else None, "traffic": None,
+                     "peak_source": "measured in this run: copy-engine pinned->HBM 1 GiB, best of 5 "
+                                    "(MEASURED_PEAKS.json has no host-link figure)",
+                     "algorithmic_bytes": moved, "device_ms": round(dma_ms, 3)},
+        "gpu_launches": int(a.steps * (2 + 2 * LAYERS) + land_launches + a.steps * LAYERS),
+        "clocks": clk, "open_s": round(t_open, 2), "dg": dg,
+        "options": {"wb_defer": a.wb_defer, "wb_stream": a.wb_stream, "spare_slots_per_layer": a.spare},
+    }
+    if not a.no_cpu_baseline and world == 1:
+        smp = a.cpu_sample_tokens
+        mv, dt = reference_sample(synth.zipf_trace(smp, LAYERS, UNITS, TOP_K, s=ZIPF, seed=1), smp)
+        line["cpu_baseline"] = {"value": round(mv / dt / 1e9, 3), "unit": "GB/s", "cores": 1, "kind": "reference",
+                                "sample": "%d tokens through the reference DgCore with a host memcpy transport "
+                                          "(oracle/_ref), %.1f s" % (smp, dt)}
+    print(json.dumps(line))
+    if dist:
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

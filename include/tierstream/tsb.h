@@ -60,6 +60,11 @@ SS_API ss_status tsb_test_dg_replay(const tsb_dg_replay_config* cfg, const int32
  * refused unless the context was opened with dg_test_hooks = 1. */
 SS_API ss_status tsb_test_dg_table(ss_ctx* c, int32_t* out, uint32_t cap);
 
+/* Host forward mode, between ss_acquire and ss_release of `layer` (test hook): per unit of the layer, out[2 u] = where
+ * its table entry points (1 = its persistent slot, 2 = a stream ring slot, 0 = no entry) and out[2 u + 1] = that slot
+ * (-1 for no entry). n must be the layer's units. */
+SS_API ss_status tsb_test_host_locs(ss_ctx* c, int layer, int32_t* out, int n);
+
 /* ---- Host xxh64 (this library's, the one the open's fill checks pinned units with; seed 0 in the descriptor) ---- */
 SS_API uint64_t tsb_xxh64(const void* data, size_t len, uint64_t seed);
 

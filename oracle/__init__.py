@@ -47,11 +47,35 @@ def ref():
         lib = C.CDLL(os.path.join(HERE, "_ref", "libtsref.so"))
         lib.oref_xxh64.restype = C.c_uint64
         lib.oref_xxh64.argtypes = [C.c_void_p, C.c_size_t, C.c_uint64]
+        lib.oref_host_replay.restype = C.c_int
+        lib.oref_host_replay.argtypes = [C.c_char_p, C.c_size_t, C.c_void_p, C.c_size_t, C.c_void_p, C.c_void_p,
+                                         C.c_uint32, C.c_void_p, C.c_uint32, C.c_void_p, C.c_void_p, C.c_void_p,
+                                         C.c_char_p, C.c_size_t]
         lib.oref_dg_replay.restype = C.c_int
         lib.oref_dg_replay.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
                                        C.c_void_p, C.c_char_p, C.c_size_t]
         _ref = lib
     return _ref
+
+
+def ref_host_replay(desc_json, tiers, budget, options, routes, all_layers):
+    """The reference's host forward mode (CPU backend) over routes [forwards][layers][n_ids]: (locs [forwards][units][2],
+    stats [forwards][layers][5] = routed, hits, admitted, transient, evicted)."""
+    import numpy as np
+    routes = np.ascontiguousarray(routes, dtype=np.int32)
+    F, L, n = routes.shape
+    total = len(tiers)
+    t = np.ascontiguousarray(tiers, dtype=np.uint8)
+    al = np.ascontiguousarray(all_layers, dtype=np.uint8)
+    locs = np.empty((F, total, 2), dtype=np.int32)
+    stats = np.empty((F, L, 5), dtype=np.uint64)
+    err = C.create_string_buffer(512)
+    raw = desc_json.encode()
+    rc = ref().oref_host_replay(raw, len(raw), t.ctypes.data, t.size, C.byref(budget), C.byref(options), F,
+                                routes.ctypes.data, n, al.ctypes.data, locs.ctypes.data, stats.ctypes.data, err, 512)
+    if rc != 0:
+        raise RuntimeError("reference host replay failed: " + err.value.decode())
+    return locs, stats
 
 
 def ref_replay(cfg, ids, preds=None, src_units=None, want_reads=False):

@@ -22,7 +22,8 @@ typedef struct oref_dg_config {
   uint32_t n_order;
   const uint32_t* order;        /* placement priority (keys) */
   uint32_t tokens, n_ids, n_pred; /* ids: [tokens][n_gated][n_ids]; preds: [tokens][n_gated][n_pred] (for g + 1) */
-  uint32_t move_bytes;          /* 1 = the transport moves real bytes (host arena and blocks) */
+  uint32_t move_bytes;          /* 1 = the transport moves real bytes (host arena and blocks); 2 = timing sample:
+                                   real copies into 4 aliased unit buffers each for slots and blocks */
 } oref_dg_config;
 
 /* Counters dumped per token (in this order). */

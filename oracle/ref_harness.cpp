@@ -19,14 +19,21 @@ class HostTransport final : public ts::DgTransport {
   HostTransport(const oref_dg_config& c, uint32_t keys, uint32_t slots)
       : parts_(c.part_bytes, c.part_bytes + c.n_parts), table_(keys, -1), move_(c.move_bytes != 0) {
     for (uint64_t b : parts_) unit_ += b;
+    // move_bytes 2: a timing sample, every copy moves its real bytes but slots and blocks alias a ring of 4 unit
+    // buffers each (the bytes read back through the table are then not meaningful)
+    alias_slots_ = c.move_bytes == 2 ? 4 : slots;
+    alias_blocks_ = c.move_bytes == 2 ? 4 : c.blocks;
     if (move_) {
-      arena_.assign(size_t(slots) * unit_, 0);
-      blocks_.assign(size_t(c.blocks) * unit_, 0);
+      arena_.assign(size_t(alias_slots_) * unit_, 1);
+      blocks_.assign(size_t(alias_blocks_) * unit_, 2);
       stage_.assign(unit_, 0);
     }
   }
-  uint8_t* slot_ptr(int32_t s) { return arena_.data() + size_t(s) * unit_; }
-  uint8_t* block_ptr(int32_t b) { return b < 0 ? stage_.data() : blocks_.data() + size_t(b) * unit_; }
+  uint8_t* slot_ptr(int32_t s) { return arena_.data() + size_t(uint32_t(s) % alias_slots_) * unit_; }
+  uint8_t* block_ptr(int32_t b) {
+    return b < 0 ? stage_.data() : blocks_.data() + size_t(uint32_t(b) % alias_blocks_) * unit_;
+  }
+  uint32_t alias_slots_ = 1, alias_blocks_ = 1;
   void h2d(Stream, int32_t slot, int32_t block) override {
     if (move_) std::memcpy(slot_ptr(slot), block_ptr(block), unit_);
   }
@@ -108,7 +115,7 @@ extern "C" __attribute__((visibility("default"))) int oref_dg_replay(const oref_
     for (uint32_t k = 0; k < keys; ++k) order.push_back(k);
     core.place(order);
     t.upload_table(core.table().data(), keys);
-    if (t.move_ && src_units)  // the open's fill: every unit into its slot or block
+    if (t.move_ && src_units && c->move_bytes == 1)  // the open's fill: every unit into its slot or block
       for (uint32_t k = 0; k < keys; ++k) {
         uint8_t* dst = core.slot_of(k) >= 0 ? t.slot_ptr(core.slot_of(k)) : t.block_ptr(core.block_of(k));
         std::memcpy(dst, src_units + size_t(k) * t.unit_, t.unit_);

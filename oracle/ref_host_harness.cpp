@@ -1,0 +1,99 @@
+// Reference harness for the host forward mode (TEST INFRASTRUCTURE): drives the reference library's own ss_* calls on
+// its CPU backend through a forward per routes row, and reads which slot each unit's table entry points at from the
+// reference context's internals (its layer pools and stream ring), so the product's tables can be compared unit for
+// unit. The product library never links this file.
+#include <atomic>
+#include <condition_variable>
+#include <cstdint>
+#include <cstdio>
+#include <cstring>
+#include <deque>
+#include <exception>
+#include <list>
+#include <memory>
+#include <mutex>
+#include <string>
+#include <thread>
+#include <vector>
+
+#include "backend.hpp"
+#include "desc.hpp"
+#include "dg_ctx.hpp"
+#include "plan.hpp"
+#include "resident_set.hpp"
+#include "source_file.hpp"
+#include "strix_stream/ss.h"
+#define private public
+#include "stream_ctx.hpp"
+#undef private
+#include "oref.h"
+
+// The reference's C ABI context (capi.cpp): a host-mode context or a device-gated one.
+struct ss_ctx {
+  std::unique_ptr<ts::Ctx> c;
+  std::unique_ptr<ts::DgCtx> dg;
+};
+
+extern "C" __attribute__((visibility("default"))) int oref_host_replay(
+    const char* desc_json, size_t len, const uint8_t* tiers, size_t n_tiers, const ss_budget* budget,
+    const ss_options* opt_in, uint32_t forwards, const int32_t* routes, uint32_t n_ids, const uint8_t* all_layers,
+    int32_t* locs, uint64_t* stats, char* err, size_t errlen) {
+  ss_desc* d = nullptr;
+  ss_plan* p = nullptr;
+  ss_ctx* c = nullptr;
+  auto bad = [&](const char* what) {
+    if (err && errlen) std::snprintf(err, errlen, "%s: %s", what, ss_last_error());
+    if (c) ss_close(c);
+    if (p) ss_plan_free(p);
+    if (d) ss_desc_free(d);
+    return -1;
+  };
+  if (ss_desc_from_json(desc_json, len, &d) != SS_OK) return bad("ss_desc_from_json");
+  if (ss_plan_from_tiers(d, budget, tiers, n_tiers, &p) != SS_OK) return bad("ss_plan_from_tiers");
+  ss_options o = *opt_in;
+  o.struct_size = sizeof o;
+  o.backend = SS_BACKEND_CPU;
+  o.forward_mode = SS_FORWARD_HOST;
+  if (ss_open(d, budget, p, &o, &c) != SS_OK) return bad("ss_open");
+  const int L_n = ss_desc_n_layers(d);
+  const int64_t total = ss_desc_total_units(d);
+  std::vector<ss_layer_stats> before(static_cast<size_t>(L_n)), after(static_cast<size_t>(L_n));
+  for (uint32_t f = 0; f < forwards; ++f) {
+    for (int L = 0; L < L_n; ++L) ss_stats_layer(c, L, &before[size_t(L)]);
+    if (ss_begin(c, nullptr, 0) != SS_OK) return bad("ss_begin");
+    int32_t* out = locs + size_t(f) * size_t(total) * 2;
+    for (int64_t k = 0; k < total * 2; ++k) out[k] = k % 2 ? -1 : 0;
+    for (int L = 0; L < L_n; ++L) {
+      const int units = ss_desc_layer_units(d, L);
+      if (units <= 0) continue;
+      const int32_t* r = routes + (size_t(f) * size_t(L_n) + size_t(L)) * n_ids;
+      const ss_status st = all_layers[L] ? ss_layer_all(c, L) : ss_layer_routes(c, L, r, int(n_ids));
+      if (st != SS_OK) return bad("routes");
+      ss_layer_view v;
+      if (ss_acquire(c, L, nullptr, &v) != SS_OK) return bad("ss_acquire");
+      const auto& s = c->c->L_[size_t(L)];
+      const int64_t base = ss_desc_unit_index(d, L, 0);
+      for (int u = 0; u < units; ++u) {
+        if (!v.table_host[u]) continue;
+        const bool ring = s.loc[size_t(u)] == ts::Ctx::Ring;
+        out[2 * (base + u)] = ring ? 2 : 1;
+        out[2 * (base + u) + 1] = ring ? s.slot[size_t(u)] : s.rs->slot(u);
+      }
+      if (ss_release(c, L, nullptr) != SS_OK) return bad("ss_release");
+    }
+    if (ss_end(c) != SS_OK) return bad("ss_end");
+    for (int L = 0; L < L_n; ++L) {
+      ss_stats_layer(c, L, &after[size_t(L)]);
+      uint64_t* o5 = stats + (size_t(f) * size_t(L_n) + size_t(L)) * 5;
+      o5[0] = after[size_t(L)].routed - before[size_t(L)].routed;
+      o5[1] = after[size_t(L)].hits - before[size_t(L)].hits;
+      o5[2] = after[size_t(L)].admitted - before[size_t(L)].admitted;
+      o5[3] = after[size_t(L)].transient - before[size_t(L)].transient;
+      o5[4] = after[size_t(L)].evicted - before[size_t(L)].evicted;
+    }
+  }
+  ss_close(c);
+  ss_plan_free(p);
+  ss_desc_free(d);
+  return 0;
+}

@@ -1,0 +1,150 @@
+"""Host forward mode on the GPU through the C ABI (C1: 8 layers x 16 experts x 3 parts of
+131072 bytes, seed 0; top-2 uniform routes from seed 1; 4 residents per layer, 12 pinned; a 4-slot ring; inclusive):
+per forward and layer, every unit's table entry points at the same slot as the reference's own host-mode context
+(its CPU backend, oracle/_ref) on the same routes, the counters match, and the bytes read through the device table
+equal the source bytes."""
+import os
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+import oracle  # noqa: E402
+from tierstream_b200 import abi, harness, runtime, synth  # noqa: E402
+
+
+@pytest.fixture(scope="module")
+def c1_model():
+    m = synth.Model(os.path.join(harness.model_dir(), "tsb-test-c1.bin"), layers=8, units=16,
+                    part_bytes=(131072, 131072, 131072), seed=0, top_k=2, with_hash=True)
+    m.write()
+    return m
+
+
+def setup(m, dynamic, pin_planned, ring=4, residents=4):
+    tiers = []
+    for _ in range(m.layers):
+        tiers += [abi.SS_TIER_RESIDENT] * residents + [abi.SS_TIER_PINNED] * (m.units - residents)
+    b = abi.budget_defaults()
+    b.device_bytes = 1 << 30
+    b.margin_gib = 1.0 / 1024
+    b.margin_fraction = 0.0
+    b.ring_slots = ring
+    b.dynamic_slots_per_layer = dynamic
+    b.host_pinned_bytes = 1 << 30
+    o = abi.options_defaults()
+    o.forward_mode = abi.SS_FORWARD_HOST
+    o.pin_planned = pin_planned
+    o.verify_hash = 1
+    return tiers, b, o
+
+
+def expected(m, orc):
+    buf = np.empty(m.unit_bytes, dtype=np.uint8)
+    out = np.zeros(m.layers * m.units, dtype=np.uint64)
+    for L in range(m.layers):
+        for u in range(m.units):
+            orc.orc_fill_bytes(m.seed, m.unit_offset(L, u), m.unit_bytes, buf.ctypes.data)
+            out[L * m.units + u] = orc.orc_checksum(buf.ctypes.data, m.unit_bytes)
+    return out
+
+
+@pytest.mark.parametrize("dynamic,pin_planned", [(0, 1), (2, 0), (3, 1)])
+def test_c1_tables_counters_and_bytes_match_reference(c1_model, orc, ref, dynamic, pin_planned):
+    m = c1_model
+    tiers, b, o = setup(m, dynamic, pin_planned)
+    routes = synth.zipf_trace(64, m.layers, m.units, 2, seed=1, uniform=True)
+    desc_json = m.desc(order="ranked")
+    ref_locs, ref_stats = oracle.ref_host_replay(desc_json, tiers, b, o, routes, [0] * m.layers)
+    desc = runtime.Desc(desc_json)
+    plan = runtime.Plan(desc, b, tiers=tiers)
+    ctx = runtime.HostContext(desc, plan, o)
+    eng = abi.load_engine()
+    want = expected(m, orc)
+    s = torch.cuda.Stream()
+    ids_dev = torch.zeros(m.units, dtype=torch.int32, device="cuda")
+    out = torch.zeros(m.units, dtype=torch.int64, device="cuda")
+    try:
+        for f in range(routes.shape[0]):
+            before = [ctx.layer_stats(L) for L in range(m.layers)]
+            ctx.begin()
+            for L in range(m.layers):
+                ctx.routes(L, routes[f, L])
+                v = ctx.acquire(L, s.cuda_stream)
+                locs = ctx.locs(L, m.units)
+                assert np.array_equal(locs, ref_locs[f, L * m.units:(L + 1) * m.units]), \
+                    "forward %d layer %d: table differs from the reference" % (f, L)
+                ids = np.unique(routes[f, L]).astype(np.int32)
+                with torch.cuda.stream(s):
+                    ids_dev[:ids.size].copy_(torch.from_numpy(ids), non_blocking=False)
+                    rc = eng.tse_read_table(C_ptr(v.table_dev), ids_dev.data_ptr(), ids.size, m.unit_bytes,
+                                            out.data_ptr(), 16, s.cuda_stream)
+                    assert rc == 0
+                s.synchronize()
+                got = out[:ids.size].cpu().numpy().astype(np.uint64)
+                assert np.array_equal(got, want[L * m.units + ids]), "forward %d layer %d: wrong bytes" % (f, L)
+                ctx.release(L, s.cuda_stream)
+            ctx.end()
+            for L in range(m.layers):
+                a = ctx.layer_stats(L)
+                mine = [a[k] - before[L][k] for k in ("routed", "hits", "admitted", "transient", "evicted")]
+                assert mine == [int(x) for x in ref_stats[f, L]], "forward %d layer %d counters" % (f, L)
+    finally:
+        ctx.close()
+
+
+def C_ptr(p):
+    import ctypes
+    return ctypes.cast(p, ctypes.c_void_p).value
+
+
+def test_layer_all_streams_blobs_through_a_two_slot_ring(orc, ref):
+    """C3-shaped, scaled: dense layer blobs, prefix order, the first layers resident, the rest streamed through a
+    2-slot ring with ss_layer_all (the Llama-3-70B config at 1 MiB + 17 byte blobs)."""
+    m = synth.Model(os.path.join(harness.model_dir(), "tsb-test-blobs.bin"), layers=12, units=1,
+                    part_bytes=((1 << 20) + 17,), seed=5, top_k=1)
+    m.write()
+    import json
+    d = json.loads(m.desc(order="prefix"))
+    for lay in d["layers"]:
+        lay["kind"] = "blob"
+        lay.pop("top_k")
+    desc_json = json.dumps(d)
+    tiers = [abi.SS_TIER_RESIDENT] * 5 + [abi.SS_TIER_PINNED] * 7
+    b = abi.budget_defaults()
+    b.device_bytes = 1 << 30
+    b.margin_gib = 1.0 / 1024
+    b.margin_fraction = 0.0
+    b.ring_slots = 2
+    b.host_pinned_bytes = 1 << 30
+    o = abi.options_defaults()
+    o.forward_mode = abi.SS_FORWARD_HOST
+    routes = np.zeros((3, m.layers, 1), dtype=np.int32)
+    ref_locs, ref_stats = oracle.ref_host_replay(desc_json, tiers, b, o, routes, [1] * m.layers)
+    desc = runtime.Desc(desc_json)
+    plan = runtime.Plan(desc, b, tiers=tiers)
+    ctx = runtime.HostContext(desc, plan, o)
+    eng = abi.load_engine()
+    want = expected(m, orc)
+    s = torch.cuda.Stream()
+    ids_dev = torch.zeros(1, dtype=torch.int32, device="cuda")
+    out = torch.zeros(1, dtype=torch.int64, device="cuda")
+    try:
+        for f in range(3):
+            ctx.begin()
+            for L in range(m.layers):
+                ctx.layer_all(L)
+                v = ctx.acquire(L, s.cuda_stream)
+                assert np.array_equal(ctx.locs(L, 1), ref_locs[f, L:L + 1])
+                with torch.cuda.stream(s):
+                    assert eng.tse_read_table(C_ptr(v.table_dev), ids_dev.data_ptr(), 1, m.unit_bytes, out.data_ptr(),
+                                              8, s.cuda_stream) == 0
+                s.synchronize()
+                assert int(out[0].item()) == int(want[L])
+                ctx.check_unit(L, 0)
+                ctx.release(L, s.cuda_stream)
+            ctx.end()
+    finally:
+        ctx.close()

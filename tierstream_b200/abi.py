@@ -197,6 +197,8 @@ _PROTOS = {
     "tsb_test_dg_replay": (C.c_int, [P(dg_replay_config), P(i32), P(i32), P(i32), P(u64), P(C.c_uint8), P(u64)]),
     "tsb_test_dg_table": (C.c_int, [vp, P(i32), u32]),
     "tsb_xxh64": (u64, [vp, C.c_size_t, u64]),
+    "tsb_test_host_locs": (C.c_int, [vp, C.c_int, P(i32), C.c_int]),
+    "ss_layer_routes_dev": (C.c_int, [vp, C.c_int, vp, C.c_int, vp]),
     "tsb_cuda_arch": (C.c_int, []),
 }
 
@@ -206,6 +208,7 @@ _ENGINE_PROTOS = {
     "tse_destroy": (C.c_int, [vp]),
     "tse_read_units": (C.c_int, [vp, u32, vp, u32, vp, u32, C.c_int, vp]),
     "tse_fill_bytes": (None, [u64, u64, u64, vp, u32]),
+    "tse_read_table": (C.c_int, [vp, vp, u32, u64, vp, u32, vp]),
 }
 
 _lib = None

@@ -595,6 +595,11 @@ ss_status tsb_test_dg_table(ss_ctx* c, int32_t* out, uint32_t cap) {
   return guard([&] { dg_of(c, "tsb_test_dg_table").test_table(out, cap); });
 }
 
+ss_status tsb_test_host_locs(ss_ctx* c, int layer, int32_t* out, int n) {
+  if (!c || !out) return SS_E_INVALID;
+  return guard([&] { host_of(c, "tsb_test_host_locs").test_locs(layer, out, n); });
+}
+
 // ---- not in this build ----
 void ss_dg_winpf_defaults_sized(ss_dg_winpf_params*, uint32_t) {}
 ss_status ss_dg_winpf_set(ss_ctx*, const ss_dg_winpf_params*) { return unsupported("ss_dg_winpf_set"); }

@@ -80,6 +80,9 @@ class HostContext {
   virtual void set_hook(ss_stats_hook hook, void* user) = 0;
   virtual void exclusive_stats(ss_exclusive_stats* out) const = 0;
   virtual std::string stats_json() const = 0;
+  // between ss_acquire and ss_release of `layer`: per unit (loc, slot) of its table entry: (1, persistent slot),
+  // (2, ring slot) or (0, -1) for no entry
+  virtual void test_locs(int layer, int32_t* out, int n) const = 0;
 };
 
 std::unique_ptr<HostContext> open_host_context(const Desc& d, const ss_budget& b, const Plan& p, const ss_options& o);

@@ -430,6 +430,7 @@ void SlotCache::serve_demand(uint32_t g, const uint32_t* ids, uint32_t n, uint64
     require(ids[i] < nu, SS_E_INVALID,
             "device-gated: layer " + std::to_string(g) + " exported id " + std::to_string(ids[i]) + " of " +
                 std::to_string(nu));
+  if (mask) m_->diag_mark(g, 0);
   // masked occurrences in export order: a repeated id is fetched at its first occurrence, covered at the others
   for (uint32_t i = 0; i < n; ++i) {
     if (!(mask >> i & 1u)) continue;
@@ -441,7 +442,10 @@ void SlotCache::serve_demand(uint32_t g, const uint32_t* ids, uint32_t n, uint64
       fetch(g, ids[i], false);
     }
   }
-  if (mask) m_->ready(g, seq_);
+  if (mask) {
+    m_->ready(g, seq_);
+    m_->diag_mark(g, 1);
+  }
 }
 
 void SlotCache::serve_use(uint32_t g, const uint32_t* ids, uint32_t n, uint64_t mask) {

@@ -55,6 +55,11 @@ class Mover {
   virtual void event_sync(void* ev) = 0;
   virtual void sync(Stream s) = 0;
   virtual void upload_table(const int32_t* table, uint32_t n) = 0;  // the whole table on kDem, then sync
+  // Timing marks on kDem for a layer with a miss: which = 0 before its first demand copy, 1 after its ready.
+  virtual void diag_mark(uint32_t g, int which) {
+    (void)g;
+    (void)which;
+  }
 };
 
 struct CacheConfig {

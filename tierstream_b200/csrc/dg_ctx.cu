@@ -262,6 +262,10 @@ class CudaMover final : public Mover {
     for (cudaStream_t s : s_)
       if (s) cudaStreamSynchronize(s);
     if (table_pin_) cudaFreeHost(table_pin_);
+    for (cudaEvent_t e : ev_a_)
+      if (e) cudaEventDestroy(e);
+    for (cudaEvent_t e : ev_b_)
+      if (e) cudaEventDestroy(e);
     for (cudaStream_t s : s_)
       if (s) cudaStreamDestroy(s);
   }
@@ -372,6 +376,38 @@ class CudaMover final : public Mover {
     flush(s);
     ck(cudaStreamWaitEvent(s_[s], ev, 0), "cudaStreamWaitEvent (test gate)");
   }
+  // dg_diag: timing events around each layer's demand work on kDem (its copies, entries and ready)
+  void enable_diag(uint32_t G) {
+    ev_a_.assign(G, nullptr);
+    ev_b_.assign(G, nullptr);
+    used_.assign(G, 0);
+    dma_ms_.assign(G, -1.0);
+    for (uint32_t g = 0; g < G; ++g) {
+      ck(cudaEventCreate(&ev_a_[g]), "cudaEventCreate (diag)");
+      ck(cudaEventCreate(&ev_b_[g]), "cudaEventCreate (diag)");
+    }
+  }
+  void diag_mark(uint32_t g, int which) override {
+    if (g >= ev_a_.size()) return;
+    flush(kDem);
+    ck(cudaEventRecord(which == 0 ? ev_a_[g] : ev_b_[g], s_[kDem]), "cudaEventRecord (diag)");
+    if (which == 1) used_[g] = 1;
+  }
+  // After the boundary synced kDem: each marked layer's demand device time; their sum is kept since open.
+  void diag_collect() {
+    for (size_t g = 0; g < used_.size(); ++g) {
+      dma_ms_[g] = -1;
+      if (!used_[g]) continue;
+      float ms = 0;
+      if (cudaEventElapsedTime(&ms, ev_a_[g], ev_b_[g]) == cudaSuccess) {
+        dma_ms_[g] = ms;
+        dma_total_ms_ += ms;
+      }
+      used_[g] = 0;
+    }
+  }
+  double dma_ms(uint32_t g) const { return g < dma_ms_.size() ? dma_ms_[g] : -1; }
+  double dma_total_ms() const { return dma_total_ms_; }
 
  private:
   char* arena(uint32_t p, int32_t slot) const { return b_.arena[p] + uint64_t(slot) * x_.part_bytes[p]; }
@@ -414,6 +450,10 @@ class CudaMover final : public Mover {
   uint64_t ce_min_ = 0;
   uint64_t launches_ = 0;
   bool deterministic_ = false;
+  std::vector<cudaEvent_t> ev_a_, ev_b_;
+  std::vector<uint8_t> used_;
+  std::vector<double> dma_ms_;
+  double dma_total_ms_ = 0;
 };
 
 // ---------------------------------------------------------------------------------------------------------------
@@ -885,6 +925,7 @@ class CudaDgContext final : public DgContext {
       t.covered_waits = l.covered_waits;
       t.gpu_wait_us = gpu_wait_us_[size_t(g)];
       t.gpu_export_ready_us = gpu_ready_us_[size_t(g)];
+      t.dma_ms = mover_->dma_ms(uint32_t(g));
     }
     std::memcpy(out, &t, sizeof t);
   }
@@ -989,13 +1030,15 @@ class CudaDgContext final : public DgContext {
                   "{\"schema\":\"strix-stream/stats-v1\",\"mode\":\"device-gated\",\"copy\":\"%s\","
                   "\"dg\":{\"tokens\":%llu,\"lookups\":%llu,\"misses\":%llu,\"covered\":%llu,\"fetched\":%llu,"
                   "\"prefetched\":%llu,\"bank_serves\":%llu,\"evicted\":%llu,\"resurrected\":%llu,"
-                  "\"writebacks_done\":%llu,\"wb_issued_bytes\":%llu,\"free_slots\":%llu,\"land_launches\":%llu}}",
+                  "\"writebacks_done\":%llu,\"wb_issued_bytes\":%llu,\"free_slots\":%llu,\"land_launches\":%llu,"
+                  "\"dma_ms_total\":%.6f,\"open_seconds\":%.3f}}",
                   mover_->kernel_copies() ? "land-kernel" : "copy-engine", (unsigned long long)s.tokens,
                   (unsigned long long)s.lookups, (unsigned long long)s.misses, (unsigned long long)s.covered,
                   (unsigned long long)s.fetched, (unsigned long long)s.prefetched, (unsigned long long)s.bank_serves,
                   (unsigned long long)s.evicted, (unsigned long long)s.resurrected,
                   (unsigned long long)s.writebacks_done, (unsigned long long)s.wb_issued_bytes,
-                  (unsigned long long)s.free_slots, (unsigned long long)mover_->kernel_launches());
+                  (unsigned long long)s.free_slots, (unsigned long long)mover_->kernel_launches(),
+                  mover_->dma_total_ms(), open_seconds_);
     return buf;
   }
   void reset_open() override {
@@ -1077,6 +1120,7 @@ class CudaDgContext final : public DgContext {
     return s + host + " (the token's outputs must be discarded; the context is poisoned)";
   }
   void collect_diag() {
+    mover_->diag_collect();
     const uint32_t G = uint32_t(x_.gated.size());
     for (uint32_t g = 0; g < G; ++g) {
       const volatile unsigned long long* t = stamps_h_ + 4u * g;
@@ -1203,6 +1247,7 @@ class CudaDgContext final : public DgContext {
     bufs_.staging_d = static_cast<char*>(sd);
     // the cache: residents in slots 0.., every other unit in a block
     mover_ = std::make_unique<CudaMover>(x_, bufs_);
+    if (o_.dg_diag) mover_->enable_diag(G);
     CacheConfig c;
     for (int L : x_.gated) c.n_units.push_back(uint32_t(d_.layers[size_t(L)].n_units));
     c.persistent_slots = x_.persistent_slots;

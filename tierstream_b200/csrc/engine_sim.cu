@@ -71,6 +71,30 @@ __global__ __launch_bounds__(kThreads) void reader_kernel(ss_dg_device_view v, u
   }
 }
 
+// Host forward mode's reader: unit ids[i] at the address table_dev[ids[i]] (ss_layer_view.table_dev), unit_bytes
+// long; the positional checksum of tests/test_cuda.cu's checksum kernel (64-75 there). A zero address reads as 0.
+__global__ __launch_bounds__(kThreads) void table_reader_kernel(const uint64_t* table, const int32_t* ids, uint32_t n,
+                                                                uint64_t unit_bytes, unsigned long long* out) {
+  const uint32_t i = blockIdx.x;
+  if (i >= n) return;
+  const uint8_t* base = reinterpret_cast<const uint8_t*>(table[ids[i]]);
+  uint64_t acc = 0;
+  if (base) {
+    const uint64_t per = (unit_bytes + gridDim.y - 1) / gridDim.y;
+    const uint64_t lo = per * blockIdx.y, hi = lo + per < unit_bytes ? lo + per : unit_bytes;
+    for (uint64_t p = lo + threadIdx.x; p < hi; p += kThreads) acc += uint64_t(base[p]) * (p % 251 + 1);
+  }
+  __shared__ uint64_t part[kThreads / 32];
+  acc = warp_sum(acc);
+  if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = acc;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    uint64_t s = 0;
+    for (int k = 0; k < kThreads / 32; ++k) s += part[k];
+    atomicAdd(out + i, (unsigned long long)s);
+  }
+}
+
 #define CK(x)                                  \
   do {                                         \
     const cudaError_t e_ = (x);                \
@@ -182,6 +206,16 @@ __attribute__((visibility("default"))) int tse_launch(void* exec, void* stream) 
 
 __attribute__((visibility("default"))) int tse_destroy(void* exec) {
   return int(cudaGraphExecDestroy(static_cast<cudaGraphExec_t>(exec)));
+}
+
+// Host forward mode: checksums of n units read through an acquired layer's device address table, on `stream`.
+__attribute__((visibility("default"))) int tse_read_table(const uint64_t* table_dev, const int32_t* ids_dev,
+                                                          uint32_t n, uint64_t unit_bytes,
+                                                          unsigned long long* out_dev, uint32_t slices, void* stream) {
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  CK(cudaMemsetAsync(out_dev, 0, size_t(n) * 8, s));
+  table_reader_kernel<<<dim3(n, slices), kThreads, 0, s>>>(table_dev, ids_dev, n, unit_bytes, out_dev);
+  return int(cudaGetLastError());
 }
 
 // The reader alone (no capture): checksums of n units of gated layer g resolved through the context's table.

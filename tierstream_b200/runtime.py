@@ -126,6 +126,58 @@ class DgContext:
         abi.check(abi.load().ss_dg_reset_open(self.h))
 
 
+class HostContext:
+    """A host forward mode context (ss_open with forward_mode = SS_FORWARD_HOST)."""
+
+    def __init__(self, desc, plan, options):
+        lib = abi.load()
+        self.desc, self.plan = desc, plan
+        self.h = C.c_void_p()
+        abi.check(lib.ss_open(desc.h, C.byref(plan.budget), plan.h, C.byref(options), C.byref(self.h)))
+
+    def close(self):
+        if getattr(self, "h", None):
+            abi.load().ss_close(self.h)
+            self.h = None
+
+    def __del__(self):
+        self.close()
+
+    def begin(self):
+        abi.check(abi.load().ss_begin(self.h, None, 0))
+
+    def routes(self, layer, ids):
+        a = np.ascontiguousarray(ids, dtype=np.int32)
+        abi.check(abi.load().ss_layer_routes(self.h, layer, a.ctypes.data_as(C.POINTER(C.c_int32)), a.size))
+
+    def layer_all(self, layer):
+        abi.check(abi.load().ss_layer_all(self.h, layer))
+
+    def acquire(self, layer, stream):
+        v = abi.ss_layer_view()
+        abi.check(abi.load().ss_acquire(self.h, layer, stream, C.byref(v)))
+        return v
+
+    def release(self, layer, stream):
+        abi.check(abi.load().ss_release(self.h, layer, stream))
+
+    def end(self):
+        abi.check(abi.load().ss_end(self.h))
+
+    def locs(self, layer, n_units):
+        out = np.empty(2 * n_units, dtype=np.int32)
+        abi.check(abi.load().tsb_test_host_locs(self.h, layer, out.ctypes.data_as(C.POINTER(C.c_int32)), n_units))
+        return out.reshape(n_units, 2)
+
+    def layer_stats(self, layer):
+        s = abi.ss_layer_stats()
+        abi.check(abi.load().ss_stats_layer(self.h, layer, C.byref(s)))
+        return {n: getattr(s, n) for n, _ in s._fields_}
+
+    def check_unit(self, layer, unit):
+        abi.check(abi.load().ss_check_unit(self.h, layer, unit))
+
+
 class TokenGraph:
     """One decode step captured once (libtsb_engine.so): begin, per layer export / wait / reader, end."""
 
