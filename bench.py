@@ -38,7 +38,13 @@ def args_():
     p.add_argument("--warmup", type=int, default=8)
     p.add_argument("--impl", default="tierstream", choices=["tierstream", "reference"])
     p.add_argument("--copy-mode", default=os.environ.get("TSB_COPY_MODE", "auto"), choices=["auto", "kernel", "ce"])
-    p.add_argument("--wb-defer", type=int, default=1, help="ss_options.dg_wb_defer (the reference default 1)")
+    p.add_argument("--wb-defer", type=int, default=0,
+                   help="ss_options.dg_wb_defer: 0 (here) enqueues a boundary's write-backs on the write-back stream "
+                        "at once, where one of B200's copy engines overlaps them with the demand copies; the "
+                        "reference's default 1 defers them part by part (tuned for a single copy engine)")
+    p.add_argument("--inclusive", type=int, default=-1,
+                   help="ss_options.dg_inclusive_blocks: device units keeping their pinned block as a clean copy "
+                        "(an eviction is then a drop, no write-back); -1 = every pinned unit")
     p.add_argument("--wb-stream", type=int, default=1, help="ss_options.dg_wb_stream (the reference default 1)")
     p.add_argument("--spare", type=int, default=SPARE, help="spare slots per layer (dynamic_slots_per_layer)")
     p.add_argument("--cpu-sample-tokens", type=int, default=6)
@@ -123,15 +129,21 @@ def h2d_peak(torch):
     return n / (best / 1e3) / 1e9
 
 
-def reference_sample(ids, tokens):
+def inclusive_of(a):
+    return LAYERS * UNITS - RESIDENTS if a.inclusive < 0 else a.inclusive
+
+
+def reference_sample(ids, tokens, a):
     """The reference DgCore + memcpy transport on `tokens` tokens of the trace (oracle/_ref): (miss bytes, seconds)."""
     import oracle
     from tierstream_b200 import runtime
     keys = resident_keys(1)
     P = LAYERS * UNITS - len(keys)
-    cfg = runtime.replay_config([UNITS] * LAYERS, [PART] * 3, persistent_slots=len(keys) + SPARE * LAYERS,
-                                bank_slots=TOP_K, blocks=P + SPARE * LAYERS, spare_target=SPARE * LAYERS,
-                                order=keys, tokens=tokens, n_ids=TOP_K, move_bytes=2)
+    inc = inclusive_of(a)
+    cfg = runtime.replay_config([UNITS] * LAYERS, [PART] * 3, persistent_slots=len(keys) + a.spare * LAYERS,
+                                bank_slots=TOP_K, blocks=P + a.spare * LAYERS + inc, spare_target=a.spare * LAYERS,
+                                order=keys, tokens=tokens, n_ids=TOP_K, move_bytes=2, wb_defer=a.wb_defer,
+                                wb_on_d2h=a.wb_stream, inclusive=inc)
     t0 = time.perf_counter()
     _, stats = oracle.ref_replay(cfg, ids[:tokens])
     dt = time.perf_counter() - t0
@@ -150,9 +162,9 @@ def run_reference(a):
         print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libtsref.so (the reference's sources "
                                                               "compiled by oracle/Makefile) is not built"}))
         return 0
-    moved, dt = reference_sample(ids, a.warmup + a.steps)
+    moved, dt = reference_sample(ids, a.warmup + a.steps, a)
     # the replay cannot split warm-up from timed tokens inside one call: time both and subtract the warm-up alone
-    w_moved, w_dt = reference_sample(ids, a.warmup) if a.warmup else (0, 0.0)
+    w_moved, w_dt = reference_sample(ids, a.warmup, a) if a.warmup else (0, 0.0)
     moved, dt = moved - w_moved, max(dt - w_dt, 1e-9)
     v = moved / dt / 1e9
     line = {"impl": "reference", "metric": METRIC, "value": round(v, 3), "unit": "GB/s", "n_gpus": a.gpus,
@@ -197,9 +209,11 @@ def main():
     barrier()
     peak = h2d_peak(torch) if rank == 0 else None
     ids = synth.zipf_trace(a.warmup + a.steps, LAYERS, UNITS, TOP_K, s=ZIPF, seed=1 + rank)
+    inclusive = inclusive_of(a)
     t_open = time.perf_counter()
     run = harness.DgRun(model, resident_keys=resident_keys(1 + rank), spare_per_layer=a.spare, max_ids=TOP_K,
-                        diag=True, test_hooks=False, mode=1, slices=128, wb_defer=a.wb_defer, wb_stream=a.wb_stream)
+                        diag=True, test_hooks=False, mode=1, slices=128, wb_defer=a.wb_defer, wb_stream=a.wb_stream,
+                        inclusive=inclusive)
     t_open = time.perf_counter() - t_open
     unit = model.unit_bytes
     try:
@@ -289,11 +303,12 @@ def main():
                      "algorithmic_bytes": moved, "device_ms": round(dma_ms, 3)},
         "gpu_launches": int(a.steps * (2 + 2 * LAYERS) + land_launches + a.steps * LAYERS),
         "clocks": clk, "open_s": round(t_open, 2), "dg": dg,
-        "options": {"wb_defer": a.wb_defer, "wb_stream": a.wb_stream, "spare_slots_per_layer": a.spare},
+        "options": {"wb_defer": a.wb_defer, "wb_stream": a.wb_stream, "spare_slots_per_layer": a.spare,
+                    "inclusive_blocks": inclusive},
     }
     if not a.no_cpu_baseline and world == 1:
         smp = a.cpu_sample_tokens
-        mv, dt = reference_sample(synth.zipf_trace(smp, LAYERS, UNITS, TOP_K, s=ZIPF, seed=1), smp)
+        mv, dt = reference_sample(synth.zipf_trace(smp, LAYERS, UNITS, TOP_K, s=ZIPF, seed=1), smp, a)
         line["cpu_baseline"] = {"value": round(mv / dt / 1e9, 3), "unit": "GB/s", "cores": 1, "kind": "reference",
                                 "sample": "%d tokens through the reference DgCore with a host memcpy transport "
                                           "(oracle/_ref), %.1f s" % (smp, dt)}

@@ -52,6 +52,7 @@ typedef struct tsb_dg_replay_config {
   const uint32_t* order;
   uint32_t tokens, n_ids, n_pred;
   uint32_t move_bytes;
+  uint32_t inclusive; /* dg_inclusive_blocks */
 } tsb_dg_replay_config;
 SS_API ss_status tsb_test_dg_replay(const tsb_dg_replay_config* cfg, const int32_t* ids, const int32_t* preds,
                                     int32_t* tables, uint64_t* stats, const uint8_t* src_units, uint64_t* read_sum);

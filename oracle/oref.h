@@ -24,6 +24,7 @@ typedef struct oref_dg_config {
   uint32_t tokens, n_ids, n_pred; /* ids: [tokens][n_gated][n_ids]; preds: [tokens][n_gated][n_pred] (for g + 1) */
   uint32_t move_bytes;          /* 1 = the transport moves real bytes (host arena and blocks); 2 = timing sample:
                                    real copies into 4 aliased unit buffers each for slots and blocks */
+  uint32_t inclusive;           /* dg_inclusive_blocks (the clean-copy share) */
 } oref_dg_config;
 
 /* Counters dumped per token (in this order). */

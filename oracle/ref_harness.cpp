@@ -106,6 +106,7 @@ extern "C" __attribute__((visibility("default"))) int oref_dg_replay(const oref_
     cfg.wb_layer_bytes = c->wb_layer_bytes;
     cfg.wb_max_outstanding = c->wb_max_outstanding;
     cfg.max_ids = c->n_ids ? c->n_ids : 1;
+    cfg.inclusive = c->inclusive;
     uint32_t keys = 0;
     for (uint32_t g = 0; g < c->n_gated; ++g) keys += c->n_units[g];
     const uint32_t slots = c->persistent_slots + 2 * c->bank_slots + 1;

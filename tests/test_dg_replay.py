@@ -41,6 +41,9 @@ CASES = {
     "one_spare_slot": dict(G=4, U=8, R=2, D=1, B=2, Q=1),
     "zero_reserve_prefetch": dict(n_pred=2, prefetch_reserve=0),
     "small_credit": dict(wb_layer_bytes=1024, wb_max_outstanding=4096),
+    "inclusive_share": dict(inclusive=5, Q=8),
+    "inclusive_share_boundary_writebacks": dict(inclusive=20, Q=24, wb_defer=0, D=2),
+    "inclusive_with_predictions": dict(inclusive=12, Q=16, n_pred=2),
 }
 
 

@@ -129,7 +129,7 @@ class dg_replay_config(C.Structure):
                 ("prefetch_reserve", u32), ("prefetch_per_layer", u32), ("prefetch_per_token", u32),
                 ("wb_defer", u32), ("wb_on_d2h", u32), ("wb_layer_bytes", u64), ("wb_max_outstanding", u64),
                 ("n_order", u32), ("order", C.POINTER(u32)), ("tokens", u32), ("n_ids", u32), ("n_pred", u32),
-                ("move_bytes", u32)]
+                ("move_bytes", u32), ("inclusive", u32)]
 
 
 P = C.POINTER

@@ -20,6 +20,8 @@ SlotCache::SlotCache(const CacheConfig& cfg, Mover* m) : c_(cfg), m_(m) {
   require(slots < 0x7fffffffull, SS_E_INVALID, "device-gated: more than 2^31 - 1 slots");
   slots_ = uint32_t(slots);
   bank_first_ = c_.persistent_slots;
+  require(c_.inclusive == 0 || c_.inclusive < c_.blocks, SS_E_INVALID,
+          "device-gated: the inclusive share must leave a block for write-backs");
   e_.assign(keys_, Entry{});
   table_.assign(keys_, -1);
   bank_key_.assign(2u * size_t(c_.bank_slots), kNil);
@@ -150,6 +152,10 @@ void SlotCache::to_host(uint32_t k) {
   if (x.block < 0) broken("a unit without a block left the device without a write-back");
   x.slot = -1;
   x.home = Home::Host;
+  if (x.backed) {
+    x.backed = false;
+    --backed_;
+  }
 }
 
 // Finished write-backs in submission order: the unit's home becomes its block and its slot is free; a discarded one
@@ -503,8 +509,14 @@ void SlotCache::end_token(const std::vector<uint32_t>& keep) {
       x.pf_done = nullptr;
     }
     if (x.block >= 0) {
-      free_blocks_.push_back(x.block);
-      x.block = -1;
+      if (backed_ < c_.inclusive) {  // inclusive share: the source block stays as a clean copy of the slot's bytes
+        x.backed = true;
+        ++backed_;
+        ++st_.inclusive_kept;
+      } else {
+        free_blocks_.push_back(x.block);
+        x.block = -1;
+      }
     }
   }
   coming_.clear();
@@ -537,6 +549,18 @@ void SlotCache::end_token(const std::vector<uint32_t>& keep) {
   };
   auto accept = [&](uint32_t k) {
     Entry& x = e_[k];
+    if (x.backed) {  // a clean copy: its block is its home again, no write-back
+      ++st_.inclusive_drops;
+      unlink(k);
+      --on_device_;
+      free_slots_.push_back(x.slot);
+      to_host(k);
+      table_[k] = -1;
+      ++st_.evicted;
+      ++lc_[gated_of(k)].evicted;
+      ++got;
+      return true;
+    }
     if (free_blocks_.empty()) {
       ++st_.evict_short;
       short_blocks = true;
@@ -767,6 +791,7 @@ void SlotCache::reset_open() {
   c_ = open_c_;
   apply_wb_defer();
   std::copy(open_e_.begin(), open_e_.end(), e_.begin());
+  backed_ = 0;  // clean copies are dropped: the open holds none
   std::copy(open_table_.begin(), open_table_.end(), table_.begin());
   free_slots_ = open_free_slots_;
   free_blocks_ = open_free_blocks_;
@@ -820,7 +845,9 @@ void SlotCache::check() const {
         if (table_[k] != x.slot) broken("a device unit's entry is not its slot");
         if (!x.listed) broken("a device unit outside the recency list");
         if (x.home == Home::Coming) take(block_used, x.block, "a coming unit without its source block");
+        else if (x.backed) take(block_used, x.block, "a clean copy without its own block");
         else if (x.block >= 0) broken("a device unit still holding a block");
+        if (x.backed && x.home != Home::Device) broken("a clean copy of a unit not on the device");
         break;
       case Home::Bank:
         take(slot_used, x.slot, "a bank unit without its own slot");

@@ -73,6 +73,9 @@ struct CacheConfig {
   uint32_t prefetch_per_layer = 4, prefetch_per_token = 48;
   bool wb_defer = false, wb_on_d2h = false;
   uint64_t wb_layer_bytes = 0, wb_max_outstanding = 0;
+  // Inclusive share (dg_inclusive_blocks): at most this many device units keep the pinned block they were promoted
+  // from as a clean copy, so their eviction is a drop with no write-back (0 = exclusive).
+  uint32_t inclusive = 0;
 };
 
 struct CacheStats {
@@ -83,6 +86,7 @@ struct CacheStats {
   uint64_t wb_issued_bytes = 0, wb_completed_bytes = 0, wb_cancelled_bytes = 0, wb_boundary_flushed_bytes = 0;
   uint64_t wb_forced_wait_ns = 0;
   uint64_t reset_moves = 0, reset_bytes = 0;
+  uint64_t inclusive_kept = 0, inclusive_drops = 0;
 };
 
 struct LayerCounts {
@@ -117,6 +121,7 @@ class SlotCache {
   uint32_t free_slots() const { return uint32_t(free_slots_.size()); }
   uint32_t free_blocks() const { return uint32_t(free_blocks_.size()); }
   uint32_t deferred() const { return uint32_t(deferred_.size()); }
+  uint32_t backed_units() const { return backed_; }
   uint64_t wb_outstanding_bytes() const { return outstanding_; }
   const CacheStats& stats() const { return st_; }
   const std::vector<LayerCounts>& layer_counts() const { return lc_; }
@@ -156,6 +161,7 @@ class SlotCache {
     int32_t slot = -1, block = -1;
     uint32_t prev = kNil, next = kNil;
     bool listed = false, wb_pending = false, via_pf = false, used = false;
+    bool backed = false;  // a device unit whose block still holds its bytes (inclusive share)
     void* pf_done = nullptr;
   };
   struct Writeback {
@@ -196,7 +202,7 @@ class SlotCache {
   std::vector<Entry> e_, open_e_;
   std::vector<int32_t> table_, open_table_;
   std::vector<int32_t> free_slots_, free_blocks_, open_free_slots_, open_free_blocks_;
-  uint32_t head_ = kNil, tail_ = kNil, on_device_ = 0;
+  uint32_t head_ = kNil, tail_ = kNil, on_device_ = 0, backed_ = 0;
   uint32_t open_head_ = kNil, open_tail_ = kNil, open_on_device_ = 0;
   std::deque<Writeback> wbs_;
   std::deque<Deferred> deferred_;

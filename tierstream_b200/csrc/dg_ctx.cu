@@ -96,7 +96,7 @@ struct Layout {
   std::vector<uint32_t> unit_base;  // G + 1
   std::vector<uint64_t> part_bytes, part_offset;
   uint64_t unit_bytes = 0, host_stride = 0;
-  uint32_t keys = 0, R = 0, D = 0, B = 0, P = 0, Q = 0;
+  uint32_t keys = 0, R = 0, D = 0, B = 0, P = 0, Q = 0, I = 0;
   uint32_t persistent_slots = 0, slots = 0, guard_slot = 0, blocks = 0;
   std::vector<uint32_t> residents;  // keys of tier R, key order
 };
@@ -117,8 +117,8 @@ Layout make_layout(const Desc& d, const Plan& p, const ss_options& o) {
   if (o.dg_wait_timeout_ms < 1) refuse(SS_E_INVALID, "dg_wait_timeout_ms must be >= 1");
   if (o.dg_wb_defer > 1) refuse(SS_E_INVALID, "dg_wb_defer must be 0 or 1");
   if (o.dg_wb_stream > 1) refuse(SS_E_INVALID, "dg_wb_stream must be 0 or 1");
-  if (o.dg_disk_tier || o.dg_disk_prefetch || o.dg_disk_staging || o.dg_disk_queue || o.dg_inclusive_blocks)
-    refuse(SS_E_UNSUPPORTED, "the three-tier placement (dg_disk_*, dg_inclusive_blocks) is not in this build");
+  if (o.dg_disk_tier || o.dg_disk_prefetch || o.dg_disk_staging || o.dg_disk_queue)
+    refuse(SS_E_UNSUPPORTED, "the three-tier placement (dg_disk_*) is not in this build");
   if (o.dg_no_admit || o.dg_clean_evict || o.dg_pf_revert_unused || o.dg_pf_strict_admit || o.dg_landing_blocks ||
       o.dg_bank_keep || o.dg_disk_queue_adapt || o.dg_prior_len || o.dg_score_profile_len)
     refuse(SS_E_UNSUPPORTED, "an opt-in device-gated policy of the reference that is not in this build is set");
@@ -201,6 +201,11 @@ Layout make_layout(const Desc& d, const Plan& p, const ss_options& o) {
     refuse(SS_E_CAPACITY, "the plan granted no spare blocks (host_spare_units asked " +
                               std::to_string(b.host_spare_units) + "): a write-back needs a free block");
   x.blocks = x.P + x.Q;
+  // the inclusive share comes out of the spare blocks: at least one stays for write-backs
+  x.I = o.dg_inclusive_blocks;
+  if (x.I && x.I >= x.Q)
+    refuse(SS_E_CAPACITY, "dg_inclusive_blocks " + std::to_string(x.I) + " must stay below the spare blocks (" +
+                              std::to_string(x.Q) + "): raise host_spare_units by the inclusive share");
   x.persistent_slots = x.R + x.D;
   const uint64_t S = uint64_t(x.persistent_slots) + 2ull * x.B + 1;
   require(S < 0x7fffffffull, SS_E_INVALID, "device-gated: more than 2^31 - 1 slots");
@@ -973,6 +978,9 @@ class CudaDgContext final : public DgContext {
     s.wb_outstanding_bytes = core_->wb_outstanding_bytes();
     s.wb_forced_wait_ns = d(c.wb_forced_wait_ns, base_.wb_forced_wait_ns);
     s.cuda_module_loading = module_loading_;
+    s.inclusive_kept = d(c.inclusive_kept, base_.inclusive_kept);
+    s.inclusive_drops = d(c.inclusive_drops, base_.inclusive_drops);
+    s.backed_units = core_->backed_units();
     std::memcpy(out, &s, sizeof s);
   }
   void layer_stats(int layer, ss_layer_stats* out) const override {
@@ -1016,7 +1024,7 @@ class CudaDgContext final : public DgContext {
     ss_exclusive_stats s{};
     s.struct_size = uint32_t(sizeof s);
     const CacheStats& c = core_->stats();
-    s.writebacks = c.evicted - c.wb_cancelled;
+    s.writebacks = c.evicted - c.wb_cancelled - c.inclusive_drops;
     s.writeback_bytes = c.wb_issued_bytes;
     s.free_blocks = core_->free_blocks();
     s.min_free_blocks = core_->free_blocks();
@@ -1265,6 +1273,7 @@ class CudaDgContext final : public DgContext {
     c.wb_on_d2h = o_.dg_wb_stream == 1;
     c.wb_layer_bytes = o_.dg_wb_layer_bytes;
     c.wb_max_outstanding = o_.dg_wb_max_outstanding;
+    c.inclusive = x_.I;
     core_ = std::make_unique<SlotCache>(c, mover_.get());
     std::vector<uint32_t> order;
     if (o_.dg_seed_n) {

@@ -92,6 +92,7 @@ void dg_replay(const tsb_dg_replay_config* c, const int32_t* ids, const int32_t*
   cfg.wb_on_d2h = c->wb_on_d2h != 0;
   cfg.wb_layer_bytes = c->wb_layer_bytes;
   cfg.wb_max_outstanding = c->wb_max_outstanding;
+  cfg.inclusive = c->inclusive;
   uint32_t keys = 0;
   for (uint32_t g = 0; g < c->n_gated; ++g) keys += c->n_units[g];
   HostMover m(std::vector<uint64_t>(c->part_bytes, c->part_bytes + c->n_parts), keys,

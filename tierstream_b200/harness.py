@@ -16,7 +16,7 @@ class DgRun:
     def __init__(self, model, residents_per_layer=None, resident_keys=None, spare_per_layer=1, max_ids=2,
                  host_spare_units=None, diag=False, test_hooks=True, wb_defer=1, wb_stream=1, verify=False,
                  n_pred=0, slices=64, mode=0, timeout_ms=10000, device_bytes=None, with_reader=True,
-                 resident_order=None):
+                 resident_order=None, inclusive=0):
         self.model = model
         G, U = model.layers, model.units
         self.G, self.U, self.n_ids, self.n_pred = G, U, max_ids, n_pred
@@ -38,7 +38,7 @@ class DgRun:
         b.tier_mode = abi.SS_TIER_MODE_EXCLUSIVE
         b.dynamic_slots_per_layer = spare_per_layer
         b.ring_slots = 2 * max_ids + 1
-        b.host_spare_units = host_spare_units if host_spare_units is not None else spare_per_layer * G
+        b.host_spare_units = host_spare_units if host_spare_units is not None else spare_per_layer * G + inclusive
         hs = (unit + 4095) // 4096 * 4096
         b.host_pinned_bytes = (G * U - len(resident_keys) + b.host_spare_units + 2) * hs + (64 << 20)
         self.desc = runtime.Desc(model.desc())
@@ -53,6 +53,7 @@ class DgRun:
         o.dg_wb_stream = wb_stream
         o.verify_hash = 1 if verify else 0
         o.dg_wait_timeout_ms = timeout_ms
+        o.dg_inclusive_blocks = inclusive
         self.ctx = runtime.DgContext(self.desc, self.plan, o)
         self.stream = torch.cuda.Stream()
         self.ids_pin = torch.zeros(G * max_ids, dtype=torch.int32).pin_memory()

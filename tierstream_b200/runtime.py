@@ -208,7 +208,7 @@ class TokenGraph:
 
 def replay_config(n_units, part_bytes, persistent_slots, bank_slots, blocks, spare_target, order, tokens, n_ids,
                   n_pred=0, prefetch_reserve=0xFFFFFFFF, prefetch_per_layer=4, prefetch_per_token=48, wb_defer=1,
-                  wb_on_d2h=1, wb_layer_bytes=0, wb_max_outstanding=0, move_bytes=0):
+                  wb_on_d2h=1, wb_layer_bytes=0, wb_max_outstanding=0, move_bytes=0, inclusive=0):
     """A dg_replay_config with its arrays kept alive on the returned object."""
     c = abi.dg_replay_config()
     keep = {}
@@ -226,7 +226,7 @@ def replay_config(n_units, part_bytes, persistent_slots, bank_slots, blocks, spa
         wb_max_outstanding
     c.n_order = len(order)
     c.order = keep["order"]
-    c.tokens, c.n_ids, c.n_pred, c.move_bytes = tokens, n_ids, n_pred, move_bytes
+    c.tokens, c.n_ids, c.n_pred, c.move_bytes, c.inclusive = tokens, n_ids, n_pred, move_bytes, inclusive
     c._keep = keep
     return c
 
