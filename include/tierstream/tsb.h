@@ -31,6 +31,17 @@ SS_API ss_status tsb_xxh64_units(const void* const* spans, const uint64_t* span_
                                  uint32_t n, void* units_dev, const uint64_t* expect_dev, uint64_t* out_dev,
                                  uint32_t* mismatches_dev, void* stream);
 
+/* ---- K3 without caller scratch (no reference counterpart) ----
+ * tsb_xxh64_units with the unit table in a device array of this library (TSB_XXH64_STATIC_MAX_UNITS units, 288 KiB)
+ * instead of caller memory: for callers that cannot allocate device memory. n above the maximum returns SS_E_INVALID.
+ * The first call on a device looks the array up (make it before any stream capture on that device). The table needs
+ * no zeroing; *mismatches_dev is added to, not cleared. One table per device: overlapping calls on a device race.
+ * Returns after the kernel finished. */
+#define TSB_XXH64_STATIC_MAX_UNITS 4096u
+SS_API ss_status tsb_xxh64_units_static(const void* const* spans, const uint64_t* span_bytes, const uint32_t* n_spans,
+                                        uint32_t n, const uint64_t* expect_dev, uint64_t* out_dev,
+                                        uint32_t* mismatches_dev, void* stream);
+
 /* ---- Deterministic replay of the device-gated slot cache on the host (test hook) ----
  * The same configuration and outputs as the reference harness's replay: this library's slot cache (dg_core.cpp)
  * driven in the service thread's order by a host mover whose events are complete when queried. tables: [tokens][keys]

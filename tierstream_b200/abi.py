@@ -194,6 +194,7 @@ _PROTOS = {
     "ss_test_dg_stop_service": (C.c_int, [vp]),
     "tsb_land": (C.c_int, [P(vp), P(vp), P(u64), u32, vp, P(u32), P(i32), u32, vp, u32, vp, u32, vp]),
     "tsb_xxh64_units": (C.c_int, [P(vp), P(u64), P(u32), u32, vp, vp, vp, vp, vp]),
+    "tsb_xxh64_units_static": (C.c_int, [P(vp), P(u64), P(u32), u32, vp, vp, vp, vp]),
     "tsb_test_dg_replay": (C.c_int, [P(dg_replay_config), P(i32), P(i32), P(i32), P(u64), P(C.c_uint8), P(u64)]),
     "tsb_test_dg_table": (C.c_int, [vp, P(i32), u32]),
     "tsb_xxh64": (u64, [vp, C.c_size_t, u64]),
