@@ -49,6 +49,12 @@ def args_():
     p.add_argument("--spare", type=int, default=SPARE, help="spare slots per layer (dynamic_slots_per_layer)")
     p.add_argument("--cpu-sample-tokens", type=int, default=6)
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--peer", action="store_true",
+                   help="the peer tier: every expert owned by one rank's HBM store (owners planned from the ranks' "
+                        "summed routing counts, one all-reduce); a miss is copied from its owner's store (NVLink for "
+                        "a peer, HBM for the rank's own) instead of pinned RAM")
+    p.add_argument("--peer-copy", default="kernel", choices=["kernel", "ce"],
+                   help="peer tier mover: the land kernel's SM loads or the copy engines")
     return p.parse_args()
 
 
@@ -207,13 +213,23 @@ def main():
     if rank == 0:
         model.write()
     barrier()
-    peak = h2d_peak(torch) if rank == 0 else None
+    peak = h2d_peak(torch) if rank == 0 and not a.peer else None
     ids = synth.zipf_trace(a.warmup + a.steps, LAYERS, UNITS, TOP_K, s=ZIPF, seed=1 + rank)
-    inclusive = inclusive_of(a)
+    inclusive = 0 if a.peer else inclusive_of(a)
     t_open = time.perf_counter()
+    setup = None
+    if a.peer:
+        import numpy as np
+        from tierstream_b200 import peer as peer_mod, runtime
+        # the planner's input: this rank's routing counts over a calibration window of its own trace distribution
+        cal = synth.zipf_trace(64, LAYERS, UNITS, TOP_K, s=ZIPF, seed=1001 + rank)
+        counts = np.bincount((np.arange(LAYERS)[None, :, None] * UNITS + cal).reshape(-1), minlength=LAYERS * UNITS)
+        setup = peer_mod.PeerSetup(runtime.Desc(model.desc()), counts, dist, world, rank, local, verify=False,
+                                   copy=1 if a.peer_copy == "ce" else 0,
+                                   collective_device=torch.device("cuda", local) if dist else None)
     run = harness.DgRun(model, resident_keys=resident_keys(1 + rank), spare_per_layer=a.spare, max_ids=TOP_K,
                         diag=True, test_hooks=False, mode=1, slices=128, wb_defer=a.wb_defer, wb_stream=a.wb_stream,
-                        inclusive=inclusive)
+                        inclusive=inclusive, peer=setup.tier if setup else None)
     t_open = time.perf_counter() - t_open
     unit = model.unit_bytes
     try:
@@ -264,8 +280,12 @@ def main():
                                          "writebacks_done", "collected_mid", "wb_forced", "wb_forced_wait_ns",
                                          "wb_boundary_flushed", "wb_deferred", "wb_cancelled", "resurrected",
                                          "wb_issued_bytes", "covered")}
+        peer_stats = json.loads(run.ctx.stats_json())["peer"]
     finally:
         run.close()
+        if setup:  # every rank's context is closed before any store is unmapped or freed
+            barrier()
+            setup.close()
 
     tot = torch.tensor([moved, moved_e2e, dev_ms, e2e_s, dma_ms], dtype=torch.float64, device="cuda")
     if dist:
@@ -296,8 +316,8 @@ def main():
                 "d2h_bytes_per_step": LAYERS * TOP_K * 8,
                 "tokens_per_s": round(a.steps * world / e2e_s_max, 3)},
         "roofline": {"bound": "link", "kernel": "miss service (demand copies + entries + ready on the demand stream)",
-                     "achieved": round(achieved, 3) if achieved else None, "peak": round(peak, 3), "unit": "GB/s",
-                     "frac": round(achieved / peak, 4) if achieved else None, "traffic": None,
+                     "achieved": round(achieved, 3) if achieved else None, "peak": round(peak, 3) if peak else None,
+                     "unit": "GB/s", "frac": round(achieved / peak, 4) if achieved and peak else None, "traffic": None,
                      "peak_source": "measured in this run: copy-engine pinned->HBM 1 GiB, best of 5 "
                                     "(MEASURED_PEAKS.json has no host-link figure)",
                      "algorithmic_bytes": moved, "device_ms": round(dma_ms, 3)},
@@ -306,6 +326,17 @@ def main():
         "options": {"wb_defer": a.wb_defer, "wb_stream": a.wb_stream, "spare_slots_per_layer": a.spare,
                     "inclusive_blocks": inclusive},
     }
+    if a.peer:
+        # every expert lives in one rank's store: a miss is an NVLink pull from a peer or an HBM copy from the
+        # rank's own store; no pinned RAM is allocated
+        line["config"].update({"workload": "mixtral-8x7b-dg-peer", "parallelism": "peer tier x%d" % world,
+                               "peer_copy": a.peer_copy})
+        line["peer"] = peer_stats
+        line["roofline"].update({
+            "bound": "nvlink", "kernel": "miss service from the stores (peer pulls over NVLink + own-store copies)",
+            "peak": 770.0, "frac": round(achieved / 770.0, 4) if achieved else None,
+            "peak_source": "peer copy 770 GB/s per direction, measured on this pool (MEASURED_PEAKS.json has no "
+                           "NVLink figure); own-store copies (HBM) are in the same time"})
     if not a.no_cpu_baseline and world == 1:
         smp = a.cpu_sample_tokens
         mv, dt = reference_sample(synth.zipf_trace(smp, LAYERS, UNITS, TOP_K, s=ZIPF, seed=1), smp, a)

@@ -84,6 +84,55 @@ SS_API uint64_t tsb_xxh64(const void* data, size_t len, uint64_t seed);
 /* 1000 x major + minor of the CUDA architecture the kernels were compiled for (100 for sm_100a). */
 SS_API int tsb_cuda_arch(void);
 
+/* ---- Peer tier (no reference counterpart: the reference declares SS_TIER_PAIR, ss.h:103, and never fetches from
+ * it) ----
+ * Gated units partitioned over the GPUs' HBM of one box. Each rank's store holds the units it owns (one device
+ * allocation, unit i at base + i x unit_bytes, parts back to back); a device-gated miss on an owned unit is copied
+ * from its owner's store (over NVLink for a peer, inside HBM for the rank's own) instead of from pinned RAM. The slot
+ * cache's decisions are those of pinned RAM (an owned unit keeps its Host home and block number); when every unit is
+ * owned, no pinned block is allocated and evictions move no bytes. Keys are gated keys (unit_base[g] + unit). */
+#define TSB_PEER_HANDLE_BYTES 64
+typedef struct tsb_peer_store tsb_peer_store;
+
+/* owner[keys] from routing counts summed over the ranks (the one exchange step is an all-reduce of these counts):
+ * keys in descending count (ties: lower key first), each to the rank with the least count assigned so far (ties:
+ * fewer units, then lower rank) among ranks below cap_units[rank] units (NULL: no cap); -1 when every rank is full
+ * (the unit stays in pinned RAM). The same counts give the same owners on every rank. */
+SS_API ss_status tsb_peer_plan(const uint64_t* counts, uint32_t keys, uint32_t world, const uint64_t* cap_units,
+                               int32_t* owner);
+/* index[keys]: each owned key's unit index in its owner's store (the owner's keys in key order), -1 if unowned;
+ * units_per_rank[world]. Either output may be NULL. */
+SS_API ss_status tsb_peer_index(const int32_t* owner, uint32_t keys, uint32_t world, int64_t* index,
+                                uint64_t* units_per_rank);
+/* This rank's store on `device`: the units with owner[k] == rank read from the descriptor's sources and, with
+ * verify and descriptor hashes, checked on the device (K3). An empty store (no unit owned) has a NULL base. */
+SS_API ss_status tsb_peer_store_create(const ss_desc* d, const int32_t* owner, uint32_t keys, int32_t rank,
+                                       int device, int verify, tsb_peer_store** out);
+SS_API void tsb_peer_store_free(tsb_peer_store* s);
+SS_API void* tsb_peer_store_base(const tsb_peer_store* s);
+SS_API uint64_t tsb_peer_store_bytes(const tsb_peer_store* s);
+/* The store's CUDA IPC handle (TSB_PEER_HANDLE_BYTES bytes), for the other ranks' processes. */
+SS_API ss_status tsb_peer_store_export(const tsb_peer_store* s, void* handle);
+/* Maps another process's store on `device` with peer access enabled; *base is its address in this process until
+ * tsb_peer_unmap. */
+SS_API ss_status tsb_peer_map(const void* handle, int device, void** base);
+SS_API ss_status tsb_peer_unmap(void* base);
+
+typedef struct tsb_peer_tier {
+  uint32_t struct_size;
+  uint32_t world;           /* ranks */
+  int32_t rank;             /* this process's rank */
+  uint32_t keys;            /* gated keys; owner covers them */
+  const int32_t* owner;     /* [keys] owning rank, -1 = pinned RAM */
+  void* const* store_base;  /* [world] each rank's store as seen from this process (its own included) */
+  uint32_t copy;            /* 0: the land kernel pulls the parts (SM loads), 1: the copy engines */
+  uint32_t reserved;
+} tsb_peer_tier;
+/* ss_open (device-gated forward mode) with the peer tier. Every store must stay allocated and mapped until
+ * ss_close. */
+SS_API ss_status tsb_open_peer(const ss_desc* d, const ss_budget* budget, const ss_plan* plan, const ss_options* opt,
+                               const tsb_peer_tier* peer, ss_ctx** out);
+
 #ifdef __cplusplus
 }
 #endif

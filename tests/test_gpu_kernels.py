@@ -126,3 +126,29 @@ def test_device_xxh64_matches_oracle(orc):
     bad[3] ^= 1
     _, mism = xxh_units(units, expect=bad)
     assert mism == 1
+
+
+def test_device_xxh64_many_units_random_layouts(orc):
+    """Many CTAs (16 units each), units of 1-4 spans whose chunk boundaries cross span boundaries, staged and
+    one-lane units mixed in one launch."""
+    rng = np.random.default_rng(12)
+    data = torch.from_numpy(rng.integers(0, 256, size=48 << 20, dtype=np.uint8)).cuda()
+    h = data.cpu().numpy()
+    base = data.data_ptr()
+    units, want, pos = [], [], 0
+    for i in range(150):
+        n_sp = int(rng.integers(1, 5))
+        spans = [int(rng.integers(1, 3000)) * 32 for _ in range(n_sp - 1)] + [int(rng.integers(0, 90000))]
+        misalign = i % 13 == 5  # a span off the 16-byte grid: the one-lane path
+        u, blob = [], []
+        for b in spans:
+            pos = (pos + 255) // 256 * 256 + (8 if misalign else 0)
+            u.append((base + pos, b))
+            blob.append(h[pos:pos + b])
+            pos += b
+        units.append(u)
+        cat = np.concatenate(blob)
+        want.append(orc.orc_xxh64(cat.ctypes.data, cat.size, 0))
+    assert pos < h.size
+    got, _ = xxh_units(units)
+    assert [int(x) for x in got] == want

@@ -1,0 +1,153 @@
+"""The peer tier on the GPU: misses on owned units are copied from the owners' stores, every unit the engine reads has
+the source bytes, and the slot table after every token equals the reference DgCore's on the same trace with the
+owned units treated as pinned-RAM homes (deterministic schedule). One GPU emulates two ranks (both stores in its
+HBM, the store addresses handed over directly); with two GPUs, two processes exchange CUDA IPC handles after an
+NCCL all-reduce of their routing counts."""
+import os
+import socket
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+import oracle  # noqa: E402
+from tierstream_b200 import harness, peer, runtime, synth  # noqa: E402
+
+
+def expected_sums(model, orc):
+    out = np.zeros(model.layers * model.units, dtype=np.uint64)
+    buf = np.empty(model.unit_bytes, dtype=np.uint8)
+    for L in range(model.layers):
+        for u in range(model.units):
+            orc.orc_fill_bytes(model.seed, model.unit_offset(L, u), model.unit_bytes, buf.ctypes.data)
+            out[L * model.units + u] = orc.orc_checksum(buf.ctypes.data, model.unit_bytes)
+    return out
+
+
+def replay_cfg_for(run, model, tokens):
+    P = model.layers * model.units - len(run.resident_keys)
+    return runtime.replay_config([model.units] * model.layers, list(model.part_bytes),
+                                 persistent_slots=len(run.resident_keys) + model.layers, bank_slots=run.n_ids,
+                                 blocks=P + model.layers, spare_target=model.layers, order=run.resident_keys,
+                                 tokens=tokens, n_ids=run.n_ids)
+
+
+def route_counts(model, ids):
+    keys = np.arange(model.layers)[None, :, None] * model.units + ids
+    return np.bincount(keys.reshape(-1), minlength=model.layers * model.units).astype(np.uint64)
+
+
+@pytest.fixture(scope="module")
+def model():
+    m = synth.Model(os.path.join(harness.model_dir(), "tsb-test-peer.bin"), layers=6, units=16,
+                    part_bytes=(2048, 2048, 4096), seed=5, top_k=2, with_hash=True)
+    m.write()
+    return m
+
+
+def check_run(run, m, ids, want, ref_tables):
+    for t in range(ids.shape[0]):
+        got = run.step(ids[t])
+        keys = np.arange(m.layers)[:, None] * m.units + ids[t]
+        assert np.array_equal(got, want[keys]), "token %d read wrong bytes" % t
+        assert np.array_equal(run.ctx.table(run.keys), ref_tables[t]), "slot table differs after token %d" % t
+
+
+@pytest.mark.parametrize("copy", [0, 1])
+@pytest.mark.parametrize("mixed", [False, True])
+def test_emulated_two_ranks(model, orc, monkeypatch, copy, mixed):
+    monkeypatch.setenv("TSB_DG_DETERMINISTIC", "1")
+    m = model
+    ids = synth.zipf_trace(40, m.layers, m.units, 2, s=1.0, seed=21)
+    counts = route_counts(m, ids[:10])
+    keys = m.layers * m.units
+    owner = peer.plan_owners(counts, 2, cap_units=[keys // 4, keys // 4] if mixed else None)
+    assert ((owner < 0).any()) == mixed
+    desc = runtime.Desc(m.desc())
+    stores = [peer.Store(desc, owner, r, 0, verify=True) for r in range(2)]
+    tier = peer.Tier(2, 0, owner, [s.base for s in stores], copy=copy)
+    run = harness.DgRun(m, residents_per_layer=3, max_ids=2, verify=True, peer=tier)
+    try:
+        open_table = run.ctx.table(run.keys).copy()
+        want = expected_sums(m, orc)
+        t_ref, s_ref = oracle.ref_replay(replay_cfg_for(run, m, ids.shape[0]), ids)
+        check_run(run, m, ids, want, t_ref)
+        st = run.ctx.stats()
+        assert st["misses"] == s_ref[-1][2] and st["fetched"] == s_ref[-1][4] and st["evicted"] == s_ref[-1][10]
+        import json
+        pj = json.loads(run.ctx.stats_json())["peer"]
+        assert pj["world"] == 2 and pj["all_owned"] == (0 if mixed else 1)
+        assert pj["peer_units"] > 0 and pj["self_units"] > 0
+        if not mixed:
+            assert pj["peer_units"] + pj["self_units"] == st["fetched"] + st["prefetched"]
+        run.ctx.check()
+        for L in range(m.layers):
+            for u in range(m.units):
+                run.ctx.check_unit(L, u)
+        run.ctx.reset_open()  # moves through the staging unit take their bytes from the stores
+        assert np.array_equal(run.ctx.table(run.keys), open_table)
+        for L in range(m.layers):
+            for u in range(m.units):
+                run.ctx.check_unit(L, u)
+    finally:
+        run.close()
+        for s in stores:
+            s.close()
+
+
+def _two_gpu_rank(rank, world, port, path, out_dir):
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ["TSB_DG_DETERMINISTIC"] = "1"
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    torch.cuda.set_device(rank)
+    import datetime
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
+                            device_id=torch.device("cuda", rank))
+    setup = run = None
+    try:
+        m = synth.Model(path, layers=6, units=16, part_bytes=(2048, 2048, 4096), seed=5, top_k=2, with_hash=True)
+        ids = synth.zipf_trace(30, m.layers, m.units, 2, s=1.0, seed=40 + rank)
+        desc = runtime.Desc(m.desc())
+        setup = peer.PeerSetup(desc, route_counts(m, ids[:10]), dist, world, rank, rank, verify=True, copy=0,
+                               collective_device=torch.device("cuda", rank))
+        run = harness.DgRun(m, residents_per_layer=3, max_ids=2, peer=setup.tier)
+        got = np.stack([run.step(ids[t]) for t in range(ids.shape[0])])
+        tables = np.stack([run.ctx.table(run.keys)])  # final table only; per-token parity is checked below
+        np.savez(os.path.join(out_dir, "r%d.npz" % rank), got=got, owner=setup.owner, table=tables[0],
+                 resident=np.array(run.resident_keys))
+        run.close()
+        run = None
+        dist.barrier()
+    finally:
+        if run:
+            run.close()
+        if setup:
+            dist.barrier()
+            setup.close()
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_two_gpus_exchange_and_pull(model, orc, tmp_path):
+    import torch.multiprocessing as mp
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    mp.start_processes(_two_gpu_rank, args=(2, port, model.path, str(tmp_path)), nprocs=2, start_method="spawn")
+    want = expected_sums(model, orc)
+    r = [np.load(tmp_path / ("r%d.npz" % i)) for i in range(2)]
+    assert np.array_equal(r[0]["owner"], r[1]["owner"])
+    for rank in range(2):
+        ids = synth.zipf_trace(30, model.layers, model.units, 2, s=1.0, seed=40 + rank)
+        keys = np.arange(model.layers)[None, :, None] * model.units + ids
+        assert np.array_equal(r[rank]["got"], want[keys]), "rank %d read wrong bytes" % rank
+        cfg = runtime.replay_config([model.units] * model.layers, list(model.part_bytes),
+                                    persistent_slots=len(r[rank]["resident"]) + model.layers, bank_slots=2,
+                                    blocks=model.layers * model.units - len(r[rank]["resident"]) + model.layers,
+                                    spare_target=model.layers, order=list(r[rank]["resident"]), tokens=30, n_ids=2)
+        t_ref, _ = oracle.ref_replay(cfg, ids)
+        assert np.array_equal(r[rank]["table"], t_ref[-1]), "rank %d slot table differs" % rank

@@ -1,0 +1,123 @@
+"""The peer tier's host logic, without a GPU: the owner planner's rules, the store index, the two-rank exchange step
+(an all-reduce of routing counts over gloo, then the same owners on every rank), and tsb_open_peer's argument checks
+(refused before any device call)."""
+import ctypes as C
+import os
+
+import numpy as np
+import pytest
+
+from tierstream_b200 import abi, harness, peer, runtime, synth
+
+
+def test_equal_counts_deal_keys_round_robin():
+    owner = peer.plan_owners(np.ones(10, dtype=np.uint64), 3)
+    assert owner.tolist() == [0, 1, 2, 0, 1, 2, 0, 1, 2, 0]
+
+
+def test_hot_keys_spread_and_loads_balance():
+    rng = np.random.default_rng(0)
+    counts = (rng.zipf(1.3, size=512) % 10000).astype(np.uint64)
+    for world in (2, 4, 8):
+        owner = peer.plan_owners(counts, world)
+        assert owner.min() == 0 and owner.max() == world - 1
+        loads = np.array([counts[owner == r].sum() for r in range(world)], dtype=np.float64)
+        # greedy on descending counts: every rank's load within the largest single count of the mean
+        assert loads.max() - loads.min() <= counts.max()
+        hottest = np.argsort(-counts.astype(np.int64), kind="stable")[:world]
+        assert sorted(owner[hottest].tolist()) == list(range(world)), "the hottest keys go to different ranks"
+
+
+def test_plan_is_deterministic_and_tie_rules():
+    counts = np.array([5, 9, 5, 0, 9, 1], dtype=np.uint64)
+    a = peer.plan_owners(counts, 2)
+    b = peer.plan_owners(counts.copy(), 2)
+    assert np.array_equal(a, b)
+    # order: 1 (9), 4 (9), 0 (5), 2 (5), 5 (1), 3 (0); loads: r0 9, r1 9 -> 0 to r0 (tie: fewer units equal, lower
+    # rank), 2 to r1, 5 to r0 (14 vs 14, units 2 vs 2 -> r0), 3 to r1 (r1 14 < r0 15)
+    assert a.tolist() == [0, 0, 1, 1, 1, 0]
+
+
+def test_capacity_and_overflow_to_pinned():
+    counts = np.arange(12, dtype=np.uint64)
+    owner = peer.plan_owners(counts, 2, cap_units=[3, 4])
+    assert (owner == 0).sum() == 3 and (owner == 1).sum() == 4 and (owner == -1).sum() == 5
+    # the unowned keys are the coldest
+    assert set(np.nonzero(owner == -1)[0].tolist()) == {0, 1, 2, 3, 4}
+
+
+def test_store_index_follows_key_order_per_owner():
+    owner = np.array([1, 0, 1, -1, 0, 1], dtype=np.int32)
+    index, per = peer.store_index(owner, 2)
+    assert index.tolist() == [0, 0, 1, -1, 1, 2]
+    assert per.tolist() == [2, 3]
+
+
+def test_bad_plan_arguments():
+    lib = abi.load()
+    counts = (C.c_uint64 * 4)(1, 2, 3, 4)
+    owner = (C.c_int32 * 4)()
+    assert lib.tsb_peer_plan(counts, 4, 0, None, owner) == abi.SS_E_INVALID
+    bad = np.array([0, 2], dtype=np.int32)
+    assert lib.tsb_peer_index(bad.ctypes.data_as(C.POINTER(C.c_int32)), 2, 2, None, None) == abi.SS_E_INVALID
+    assert b"not a rank below the world size" in lib.ss_last_error()
+
+
+def _rank_main(rank, world, port, out_dir):
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        ids = synth.zipf_trace(20, 4, 16, 2, s=1.1, seed=100 + rank)  # each rank routes its own trace
+        local = np.bincount((np.arange(4)[None, :, None] * 16 + ids).reshape(-1), minlength=64)
+        counts = peer.all_reduce_counts(local, dist)
+        owner = peer.plan_owners(counts, world)
+        handles = peer.all_gather_handles(bytes([rank]) * 64, dist, world)
+        np.save(os.path.join(out_dir, "r%d.npy" % rank), np.concatenate([counts.astype(np.int64), owner]))
+        assert [h[0] for h in handles] == list(range(world))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_two_ranks_plan_the_same_owners(tmp_path):
+    import socket
+
+    import torch.multiprocessing as mp
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    mp.start_processes(_rank_main, args=(2, port, str(tmp_path)), nprocs=2, start_method="spawn")
+    r0, r1 = np.load(tmp_path / "r0.npy"), np.load(tmp_path / "r1.npy")
+    assert np.array_equal(r0, r1)
+    want = np.zeros(64, dtype=np.int64)
+    for r in range(2):
+        ids = synth.zipf_trace(20, 4, 16, 2, s=1.1, seed=100 + r)
+        want += np.bincount((np.arange(4)[None, :, None] * 16 + ids).reshape(-1), minlength=64)
+    assert np.array_equal(r0[:64], want)
+    assert np.array_equal(r0[64:], peer.plan_owners(want.astype(np.uint64), 2))
+
+
+def test_open_peer_refuses_bad_tiers():
+    m = synth.Model(os.path.join(harness.model_dir(), "tsb-peer-args.bin"), layers=2, units=4,
+                    part_bytes=(256, 256, 256), seed=1)
+    desc = runtime.Desc(m.desc())
+    lib = abi.load()
+    b = abi.budget_defaults()
+    o = abi.options_defaults()
+    o.forward_mode = abi.SS_FORWARD_DEVICE_GATED
+    owner = np.zeros(8, dtype=np.int32)
+
+    def opened(tier):
+        h = C.c_void_p()
+        t = tier.struct()
+        return lib.tsb_open_peer(desc.h, C.byref(b), None, C.byref(o), C.byref(t), C.byref(h))
+
+    assert opened(peer.Tier(2, 2, owner, [0, 0])) == abi.SS_E_INVALID  # rank outside the world
+    assert b"rank outside" in lib.ss_last_error()
+    assert opened(peer.Tier(2, 0, owner[:6], [0, 0])) == abi.SS_E_INVALID  # fewer keys than gated units
+    assert b"gated units" in lib.ss_last_error()
+    assert opened(peer.Tier(1, 0, owner, [0])) == abi.SS_E_INVALID  # rank 0 owns units but has no store
+    assert b"store_base is null" in lib.ss_last_error()
+    t = peer.Tier(1, 0, owner, [0x1000], copy=2)
+    assert opened(t) == abi.SS_E_INVALID

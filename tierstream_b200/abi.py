@@ -132,6 +132,14 @@ class dg_replay_config(C.Structure):
                 ("move_bytes", u32), ("inclusive", u32)]
 
 
+class tsb_peer_tier(C.Structure):
+    """tsb_peer_tier (include/tierstream/tsb.h): the peer tier's owners and store addresses for tsb_open_peer."""
+    _fields_ = [("struct_size", u32), ("world", u32), ("rank", C.c_int32), ("keys", u32),
+                ("owner", C.POINTER(C.c_int32)), ("store_base", C.POINTER(vp)), ("copy", u32), ("reserved", u32)]
+
+
+PEER_HANDLE_BYTES = 64
+
 P = C.POINTER
 _PROTOS = {
     "ss_last_error": (C.c_char_p, []),
@@ -195,6 +203,16 @@ _PROTOS = {
     "tsb_land": (C.c_int, [P(vp), P(vp), P(u64), u32, vp, P(u32), P(i32), u32, vp, u32, vp, u32, vp]),
     "tsb_xxh64_units": (C.c_int, [P(vp), P(u64), P(u32), u32, vp, vp, vp, vp, vp]),
     "tsb_xxh64_units_static": (C.c_int, [P(vp), P(u64), P(u32), u32, vp, vp, vp, vp]),
+    "tsb_peer_plan": (C.c_int, [P(u64), u32, u32, P(u64), P(C.c_int32)]),
+    "tsb_peer_index": (C.c_int, [P(C.c_int32), u32, u32, P(i64), P(u64)]),
+    "tsb_peer_store_create": (C.c_int, [vp, P(C.c_int32), u32, C.c_int32, C.c_int, C.c_int, P(vp)]),
+    "tsb_peer_store_free": (None, [vp]),
+    "tsb_peer_store_base": (vp, [vp]),
+    "tsb_peer_store_bytes": (u64, [vp]),
+    "tsb_peer_store_export": (C.c_int, [vp, vp]),
+    "tsb_peer_map": (C.c_int, [vp, C.c_int, P(vp)]),
+    "tsb_peer_unmap": (C.c_int, [vp]),
+    "tsb_open_peer": (C.c_int, [vp, P(ss_budget), vp, P(ss_options), P(tsb_peer_tier), P(vp)]),
     "tsb_test_dg_replay": (C.c_int, [P(dg_replay_config), P(i32), P(i32), P(i32), P(u64), P(C.c_uint8), P(u64)]),
     "tsb_test_dg_table": (C.c_int, [vp, P(i32), u32]),
     "tsb_xxh64": (u64, [vp, C.c_size_t, u64]),

@@ -12,6 +12,7 @@
 #include "desc.hpp"
 #include "errors.hpp"
 #include "json.hpp"
+#include "peer.hpp"
 #include "plan.hpp"
 #include "strix_stream/ss.h"
 #include "strix_stream/ss_test.h"
@@ -307,7 +308,9 @@ ss_status ss_plan_to_json(const ss_plan* p, char** out_json, size_t* out_len) {
 // ---- context ----
 void ss_options_defaults_sized(ss_options* o, uint32_t size) { sized_defaults(o, size, options_defaults); }
 
-ss_status ss_open(const ss_desc* d, const ss_budget* budget, const ss_plan* plan, const ss_options* opt, ss_ctx** out) {
+namespace {
+ss_status open_impl(const ss_desc* d, const ss_budget* budget, const ss_plan* plan, const ss_options* opt,
+                    const tsb::PeerTier* peer, ss_ctx** out) {
   return guard([&] {
     need(d && budget && out, "ss_open: null argument");
     need(!plan || plan->desc == d, "ss_open: plan was made from another descriptor");
@@ -328,14 +331,20 @@ ss_status ss_open(const ss_desc* d, const ss_budget* budget, const ss_plan* plan
     const tsb::Plan p = plan ? plan->p : tsb::plan_make(d->d, bb, {});
     need(o.forward_mode == SS_FORWARD_HOST || o.forward_mode == SS_FORWARD_DEVICE_GATED, "ss_open: unknown forward_mode");
     if (o.forward_mode == SS_FORWARD_DEVICE_GATED) {
-      auto dg = tsb::open_dg_context(d->d, p, o);
+      auto dg = tsb::open_dg_context(d->d, p, o, peer);
       *out = new ss_ctx{nullptr, std::move(dg)};
     } else {
+      need(!peer, "tsb_open_peer: the peer tier serves device-gated decode only (forward_mode DEVICE_GATED)");
       need(o.policy == SS_POLICY_LRU, "ss_open: host mode supports SS_POLICY_LRU in this build");
       auto h = tsb::open_host_context(d->d, bb, p, o);
       *out = new ss_ctx{std::move(h), nullptr};
     }
   });
+}
+}  // namespace
+
+ss_status ss_open(const ss_desc* d, const ss_budget* budget, const ss_plan* plan, const ss_options* opt, ss_ctx** out) {
+  return open_impl(d, budget, plan, opt, nullptr, out);
 }
 void ss_close(ss_ctx* c) { delete c; }
 int ss_source_direct(const ss_ctx* c, int source) {
@@ -598,6 +607,92 @@ ss_status tsb_test_dg_table(ss_ctx* c, int32_t* out, uint32_t cap) {
 ss_status tsb_test_host_locs(ss_ctx* c, int layer, int32_t* out, int n) {
   if (!c || !out) return SS_E_INVALID;
   return guard([&] { host_of(c, "tsb_test_host_locs").test_locs(layer, out, n); });
+}
+
+// ---- peer tier (tsb.h) ----
+struct tsb_peer_store {
+  std::unique_ptr<tsb::PeerStore> s;
+};
+
+ss_status tsb_peer_plan(const uint64_t* counts, uint32_t keys, uint32_t world, const uint64_t* cap_units,
+                        int32_t* owner) {
+  return guard([&] {
+    need(owner || !keys, "tsb_peer_plan: null owner output");
+    const std::vector<int32_t> o = tsb::plan_owners(counts, keys, world, cap_units);
+    std::copy(o.begin(), o.end(), owner);
+  });
+}
+
+ss_status tsb_peer_index(const int32_t* owner, uint32_t keys, uint32_t world, int64_t* index,
+                         uint64_t* units_per_rank) {
+  return guard([&] {
+    need(owner || !keys, "tsb_peer_index: null owner");
+    need(world >= 1, "tsb_peer_index: world must be >= 1");
+    std::vector<uint64_t> per;
+    const std::vector<int64_t> ix = tsb::store_index(std::vector<int32_t>(owner, owner + keys), world, &per);
+    if (index) std::copy(ix.begin(), ix.end(), index);
+    if (units_per_rank) std::copy(per.begin(), per.end(), units_per_rank);
+  });
+}
+
+ss_status tsb_peer_store_create(const ss_desc* d, const int32_t* owner, uint32_t keys, int32_t rank, int device,
+                                int verify, tsb_peer_store** out) {
+  return guard([&] {
+    need(d && owner && out, "tsb_peer_store_create: null argument");
+    *out = nullptr;
+    auto s = std::make_unique<tsb_peer_store>();
+    s->s = std::make_unique<tsb::PeerStore>(d->d, std::vector<int32_t>(owner, owner + keys), rank, device, verify != 0);
+    *out = s.release();
+  });
+}
+void tsb_peer_store_free(tsb_peer_store* s) { delete s; }
+void* tsb_peer_store_base(const tsb_peer_store* s) { return s && s->s ? s->s->base() : nullptr; }
+uint64_t tsb_peer_store_bytes(const tsb_peer_store* s) { return s && s->s ? s->s->bytes() : 0; }
+ss_status tsb_peer_store_export(const tsb_peer_store* s, void* handle) {
+  return guard([&] {
+    need(s && s->s, "tsb_peer_store_export: null store");
+    tsb::ipc_export(s->s->base(), handle);
+  });
+}
+ss_status tsb_peer_map(const void* handle, int device, void** base) {
+  return guard([&] {
+    need(handle && base, "tsb_peer_map: null argument");
+    *base = tsb::ipc_map(handle, device);
+  });
+}
+ss_status tsb_peer_unmap(void* base) {
+  return guard([&] { tsb::ipc_unmap(base); });
+}
+
+ss_status tsb_open_peer(const ss_desc* d, const ss_budget* budget, const ss_plan* plan, const ss_options* opt,
+                        const tsb_peer_tier* peer, ss_ctx** out) {
+  tsb::PeerTier t;
+  const ss_status st = guard([&] {
+    need(d && peer, "tsb_open_peer: null argument");
+    need(peer->struct_size >= sizeof(tsb_peer_tier), "tsb_peer_tier: struct_size is smaller than this build's");
+    need(peer->world >= 1, "tsb_peer_tier: world must be >= 1");
+    need(peer->rank >= 0 && uint32_t(peer->rank) < peer->world, "tsb_peer_tier: rank outside [0, world)");
+    need(peer->copy <= 1, "tsb_peer_tier: copy must be 0 (land kernel) or 1 (copy engines)");
+    need(peer->owner && peer->store_base, "tsb_peer_tier: null owner or store_base");
+    const tsb::GatedKeys gk = tsb::gated_keys(d->d);
+    tsb::require(peer->keys == gk.keys(), SS_E_INVALID,
+                 "tsb_peer_tier: keys " + std::to_string(peer->keys) + " where the descriptor has " +
+                     std::to_string(gk.keys()) + " gated units");
+    t.world = peer->world;
+    t.rank = peer->rank;
+    t.copy = int(peer->copy);
+    t.owner.assign(peer->owner, peer->owner + peer->keys);
+    std::vector<uint64_t> per;
+    t.index = tsb::store_index(t.owner, t.world, &per);
+    for (uint32_t r = 0; r < peer->world; ++r) t.base.push_back(static_cast<char*>(peer->store_base[r]));
+    for (uint32_t r = 0; r < t.world; ++r)
+      tsb::require(!per[r] || t.base[r], SS_E_INVALID,
+                   "tsb_peer_tier: rank " + std::to_string(r) + " owns " + std::to_string(per[r]) +
+                       " units but its store_base is null");
+    t.all_owned = std::all_of(t.owner.begin(), t.owner.end(), [](int32_t o) { return o >= 0; });
+  });
+  if (st != SS_OK) return st;
+  return open_impl(d, budget, plan, opt, &t, out);
 }
 
 // ---- not in this build ----

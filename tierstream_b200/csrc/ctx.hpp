@@ -55,7 +55,10 @@ class DgContext {
   virtual uint32_t test_table(int32_t* out, uint32_t cap) = 0;  // the device's slot table; returns the key count
 };
 
-std::unique_ptr<DgContext> open_dg_context(const Desc& d, const Plan& p, const ss_options& o);
+struct PeerTier;
+// peer: the peer tier (peer.hpp), or null for pinned RAM only.
+std::unique_ptr<DgContext> open_dg_context(const Desc& d, const Plan& p, const ss_options& o,
+                                           const PeerTier* peer = nullptr);
 
 class HostContext {
  public:

@@ -187,7 +187,7 @@ uint32_t SlotCache::collect() {
 
 void SlotCache::submit_part(Deferred& d) {
   const uint32_t p = d.parts_done;
-  m_->d2h(wb_stream_, d.slot, d.block, int32_t(p));
+  m_->d2h(wb_stream_, d.slot, d.block, int32_t(p), d.key);
   ++d.parts_done;
   const uint64_t b = m_->part_bytes(p);
   d.bytes += b;
@@ -362,9 +362,9 @@ bool SlotCache::fetch(uint32_t g, uint32_t unit, bool prefetch) {
   const Mover::Stream s = prefetch ? Mover::kPf : Mover::kDem;
   if (mut_ == kEntryBeforeCopy) {  // test-only fault: the entry before its bytes
     publish(s, k, slot);
-    m_->h2d(s, slot, x.block);
+    m_->h2d(s, slot, x.block, k);
   } else {
-    m_->h2d(s, slot, x.block);
+    m_->h2d(s, slot, x.block, k);
     publish(s, k, slot);
   }
   x.slot = slot;
@@ -614,7 +614,7 @@ void SlotCache::end_token(const std::vector<uint32_t>& keep) {
   for (size_t i = 0; !c_.wb_defer && i < n_evict; ++i) {
     const uint32_t k = victims_[i];
     const Entry& x = e_[k];
-    m_->d2h(Mover::kD2h, x.slot, x.block, -1);
+    m_->d2h(Mover::kD2h, x.slot, x.block, -1, k);
     void* ev = event();
     m_->record(ev, Mover::kD2h);
     wbs_.push_back({k, x.slot, x.block, ev, false, unit_bytes_});
@@ -636,7 +636,7 @@ uint32_t SlotCache::seed(const std::vector<uint32_t>& keys) {
     if (x.home != Home::Host || free_slots_.size() <= c_.spare_target) continue;
     const int32_t slot = free_slots_.back();
     free_slots_.pop_back();
-    m_->h2d(Mover::kDem, slot, x.block);
+    m_->h2d(Mover::kDem, slot, x.block, k);
     free_blocks_.push_back(x.block);
     x.block = -1;
     x.slot = slot;
@@ -724,12 +724,13 @@ void SlotCache::reset_open() {
   // launches: a move's wave is one after every earlier move that reads its destination or writes its source
   struct Move {
     size_t from, to;
+    uint32_t key;
   };
   std::vector<Move> plan;
   auto move = [&](uint32_t k, size_t to) {
     const size_t from = cur[k];
     if (to > N || occupant[to] != kNil) broken("reset would overwrite a live source");
-    plan.push_back({from, to});
+    plan.push_back({from, to, k});
     occupant[from] = kNil;
     occupant[to] = k;
     cur[k] = to;
@@ -778,13 +779,13 @@ void SlotCache::reset_open() {
     }
     flush_d2d();
     if (mv.from < P) {
-      m_->d2h(Mover::kD2h, int32_t(mv.from), blk(mv.to), -1);
+      m_->d2h(Mover::kD2h, int32_t(mv.from), blk(mv.to), -1, mv.key);
       m_->sync(Mover::kD2h);
     } else if (mv.to < P) {
-      m_->h2d(Mover::kDem, int32_t(mv.to), blk(mv.from));
+      m_->h2d(Mover::kDem, int32_t(mv.to), blk(mv.from), mv.key);
       m_->sync(Mover::kDem);
     } else {
-      m_->h2h(blk(mv.from), blk(mv.to));
+      m_->h2h(blk(mv.from), blk(mv.to), mv.key);
     }
   }
   flush_d2d();

@@ -35,14 +35,14 @@ class Mover {
   virtual ~Mover() = default;
   virtual uint32_t parts() const = 0;
   virtual uint64_t part_bytes(uint32_t p) const = 0;
-  // Every part of `block` into `slot` (block -1 = the one-unit reset staging buffer).
-  virtual void h2d(Stream s, int32_t slot, int32_t block) = 0;
-  // Part p (p < 0: every part) of `slot` into `block`.
-  virtual void d2h(Stream s, int32_t slot, int32_t block, int32_t p) = 0;
+  // Every part of unit `key`, held by `block`, into `slot` (block -1 = the one-unit reset staging buffer).
+  virtual void h2d(Stream s, int32_t slot, int32_t block, uint32_t key) = 0;
+  // Part p (p < 0: every part) of unit `key`, held by `slot`, into `block`.
+  virtual void d2h(Stream s, int32_t slot, int32_t block, int32_t p, uint32_t key) = 0;
   // Reset: slot-to-slot moves (src, dst). Moves of one wave touch disjoint slots and run together; waves run in
   // ascending order. Complete when the call returns.
   virtual void d2d_moves(const std::vector<std::pair<int32_t, int32_t>>& moves, const std::vector<uint32_t>& wave) = 0;
-  virtual void h2h(int32_t src_block, int32_t dst_block) = 0;
+  virtual void h2h(int32_t src_block, int32_t dst_block, uint32_t key) = 0;
   // slot_of[key] = v after everything enqueued on s so far (a release at system scope).
   virtual void publish(Stream s, uint32_t key, int32_t v) = 0;
   // ready[g] = seq on kDem after everything enqueued there.

@@ -28,6 +28,7 @@
 #include "dg_core.hpp"
 #include "errors.hpp"
 #include "kernels.hpp"
+#include "peer.hpp"
 #include "source_file.hpp"
 #include "xxh64.hpp"
 
@@ -101,7 +102,7 @@ struct Layout {
   std::vector<uint32_t> residents;  // keys of tier R, key order
 };
 
-Layout make_layout(const Desc& d, const Plan& p, const ss_options& o) {
+Layout make_layout(const Desc& d, const Plan& p, const ss_options& o, const PeerTier* peer) {
   auto refuse = [](ss_status st, const std::string& why) { fail(st, "device-gated: " + why); };
   const ss_budget& b = p.budget;
   if (b.tier_mode != SS_TIER_MODE_EXCLUSIVE) refuse(SS_E_INVALID, "needs tier_mode EXCLUSIVE");
@@ -221,7 +222,8 @@ Layout make_layout(const Desc& d, const Plan& p, const ss_options& o) {
   if (other + need > limit)
     refuse(SS_E_CAPACITY, "the arena needs " + std::to_string(need) + " bytes where the plan billed " +
                               std::to_string(billed) + "; with the rest of the plan that is above the cap - margin");
-  if (p.pinned + x.host_stride + (uint64_t(1) << 20) > b.host_pinned_bytes)
+  const bool no_blocks = peer && peer->all_owned;  // every unit in a store: no pinned block is allocated
+  if (!no_blocks && p.pinned + x.host_stride + (uint64_t(1) << 20) > b.host_pinned_bytes)
     refuse(SS_E_CAPACITY, "the plan's pinned bytes plus the staging unit and the mapped control area exceed the host "
                           "budget (" + std::to_string(b.host_pinned_bytes) + ")");
   return x;
@@ -243,7 +245,7 @@ class CudaMover final : public Mover {
     uint32_t* counters = nullptr; // device, 3 (one per stream)
   };
 
-  CudaMover(const Layout& x, const Buffers& b) : x_(x), b_(b) {
+  CudaMover(const Layout& x, const Buffers& b, const PeerTier* peer) : x_(x), b_(b), peer_(peer) {
     int lo = 0, hi = 0;
     ck(cudaDeviceGetStreamPriorityRange(&lo, &hi), "cudaDeviceGetStreamPriorityRange");
     ck(cudaStreamCreateWithPriority(&s_[kDem], cudaStreamNonBlocking, hi), "cudaStreamCreate (demand)");
@@ -276,17 +278,37 @@ class CudaMover final : public Mover {
   }
   cudaStream_t stream(Stream s) const { return s_[s]; }
   bool deterministic() const { return deterministic_; }
-  bool kernel_copies() const { return ce_min_ > x_.part_bytes[0]; }
+  bool kernel_copies() const {
+    return (peer_ && peer_->all_owned && peer_->copy == 0) || ce_min_ > x_.part_bytes[0];
+  }
   uint64_t kernel_launches() const { return launches_; }
+  uint64_t peer_units() const { return peer_units_; }
+  uint64_t self_units() const { return self_units_; }
 
   uint32_t parts() const override { return uint32_t(x_.part_bytes.size()); }
   uint64_t part_bytes(uint32_t p) const override { return x_.part_bytes[p]; }
 
-  void h2d(Stream s, int32_t slot, int32_t block) override {
+  void h2d(Stream s, int32_t slot, int32_t block, uint32_t key) override {
+    if (peer_ && peer_->owned(key)) {  // from the owner's store: NVLink for a peer, HBM for this GPU's own
+      const char* src = peer_->src(key, x_.unit_bytes);
+      const bool self = peer_->owner[key] == peer_->rank;
+      for (uint32_t p = 0; p < parts(); ++p) {
+        if (peer_->copy == 1) {
+          flush(s);
+          ck(cudaMemcpyAsync(arena(p, slot), src + x_.part_offset[p], size_t(x_.part_bytes[p]), cudaMemcpyDefault, s_[s]),
+             "cudaMemcpyAsync (store part)");
+        } else {
+          add_copy(s, src + x_.part_offset[p], arena(p, slot), x_.part_bytes[p]);
+        }
+      }
+      ++(self ? self_units_ : peer_units_);
+      return;
+    }
     for (uint32_t p = 0; p < parts(); ++p)
       copy(s, block_dev(block) + x_.part_offset[p], arena(p, slot), x_.part_bytes[p], cudaMemcpyHostToDevice);
   }
-  void d2h(Stream s, int32_t slot, int32_t block, int32_t part) override {
+  void d2h(Stream s, int32_t slot, int32_t block, int32_t part, uint32_t key) override {
+    if (peer_ && peer_->owned(key)) return;  // its store keeps its bytes: the block is bookkeeping only
     for (uint32_t p = 0; p < parts(); ++p) {
       if (part >= 0 && uint32_t(part) != p) continue;
       copy(s, arena(p, slot), block_dev(block) + x_.part_offset[p], x_.part_bytes[p], cudaMemcpyDeviceToHost);
@@ -306,7 +328,8 @@ class CudaMover final : public Mover {
     }
     sync(kDem);
   }
-  void h2h(int32_t src, int32_t dst) override {
+  void h2h(int32_t src, int32_t dst, uint32_t key) override {
+    if (peer_ && peer_->owned(key)) return;
     std::memcpy(block_host(dst), block_host(src), size_t(x_.unit_bytes));
   }
   void publish(Stream s, uint32_t key, int32_t v) override {
@@ -448,6 +471,8 @@ class CudaMover final : public Mover {
 
   const Layout& x_;
   Buffers b_;
+  const PeerTier* peer_ = nullptr;
+  uint64_t peer_units_ = 0, self_units_ = 0;
   cudaStream_t s_[3] = {nullptr, nullptr, nullptr};
   int32_t* table_pin_ = nullptr;
   std::unique_ptr<dev::Batch> batch_[3];
@@ -696,7 +721,8 @@ class Service {
 // ---------------------------------------------------------------------------------------------------------------
 class CudaDgContext final : public DgContext {
  public:
-  CudaDgContext(const Desc& d, const Plan& p, const ss_options& o) : d_(d), o_(o), x_(make_layout(d, p, o)) {
+  CudaDgContext(const Desc& d, const Plan& p, const ss_options& o, const PeerTier* peer)
+      : d_(d), o_(o), peer_(peer ? std::make_unique<PeerTier>(*peer) : nullptr), x_(make_layout(d, p, o, peer)) {
     try {
       init();
     } catch (...) {
@@ -816,6 +842,8 @@ class CudaDgContext final : public DgContext {
         ck(cudaMemcpy(got.data() + x_.part_offset[p], bufs_.arena[p] + uint64_t(core_->slot_of(k)) * x_.part_bytes[p],
                       size_t(x_.part_bytes[p]), cudaMemcpyDeviceToHost),
            "cudaMemcpy (check)");
+    } else if (peer_ && peer_->owned(k)) {  // a Host home whose bytes live in a store
+      ck(cudaMemcpy(got.data(), peer_->src(k, x_.unit_bytes), got.size(), cudaMemcpyDefault), "cudaMemcpy (check)");
     } else {
       std::memcpy(got.data(), bufs_.blocks[size_t(core_->block_of(k))], got.size());
     }
@@ -1039,14 +1067,17 @@ class CudaDgContext final : public DgContext {
                   "\"dg\":{\"tokens\":%llu,\"lookups\":%llu,\"misses\":%llu,\"covered\":%llu,\"fetched\":%llu,"
                   "\"prefetched\":%llu,\"bank_serves\":%llu,\"evicted\":%llu,\"resurrected\":%llu,"
                   "\"writebacks_done\":%llu,\"wb_issued_bytes\":%llu,\"free_slots\":%llu,\"land_launches\":%llu,"
-                  "\"dma_ms_total\":%.6f,\"open_seconds\":%.3f}}",
+                  "\"dma_ms_total\":%.6f,\"open_seconds\":%.3f},\"peer\":{\"world\":%u,\"rank\":%d,"
+                  "\"all_owned\":%d,\"copy\":\"%s\",\"peer_units\":%llu,\"self_units\":%llu}}",
                   mover_->kernel_copies() ? "land-kernel" : "copy-engine", (unsigned long long)s.tokens,
                   (unsigned long long)s.lookups, (unsigned long long)s.misses, (unsigned long long)s.covered,
                   (unsigned long long)s.fetched, (unsigned long long)s.prefetched, (unsigned long long)s.bank_serves,
                   (unsigned long long)s.evicted, (unsigned long long)s.resurrected,
                   (unsigned long long)s.writebacks_done, (unsigned long long)s.wb_issued_bytes,
                   (unsigned long long)s.free_slots, (unsigned long long)mover_->kernel_launches(),
-                  mover_->dma_total_ms(), open_seconds_);
+                  mover_->dma_total_ms(), open_seconds_, peer_ ? peer_->world : 0u, peer_ ? peer_->rank : -1,
+                  peer_ && peer_->all_owned ? 1 : 0, peer_ && peer_->copy == 1 ? "copy-engine" : "land-kernel",
+                  (unsigned long long)mover_->peer_units(), (unsigned long long)mover_->self_units());
     return buf;
   }
   void reset_open() override {
@@ -1235,7 +1266,7 @@ class CudaDgContext final : public DgContext {
     // pinned blocks (mapped: the land kernel reads them), <= 1 GiB chunks; the reset staging unit
     const uint64_t hs = x_.host_stride;
     const uint64_t per_chunk = std::max<uint64_t>(1, (uint64_t(1) << 30) / hs);
-    for (uint64_t left = x_.blocks; left > 0;) {
+    for (uint64_t left = peer_ && peer_->all_owned ? 0 : x_.blocks; left > 0;) {
       const uint64_t n = std::min(per_chunk, left);
       void* p = nullptr;
       ck(cudaHostAlloc(&p, size_t(n * hs), cudaHostAllocMapped | cudaHostAllocPortable), "cudaHostAlloc (blocks)");
@@ -1254,7 +1285,7 @@ class CudaDgContext final : public DgContext {
     ck(cudaHostGetDevicePointer(&sd, bufs_.staging, 0), "cudaHostGetDevicePointer (staging)");
     bufs_.staging_d = static_cast<char*>(sd);
     // the cache: residents in slots 0.., every other unit in a block
-    mover_ = std::make_unique<CudaMover>(x_, bufs_);
+    mover_ = std::make_unique<CudaMover>(x_, bufs_, peer_.get());
     if (o_.dg_diag) mover_->enable_diag(G);
     CacheConfig c;
     for (int L : x_.gated) c.n_units.push_back(uint32_t(d_.layers[size_t(L)].n_units));
@@ -1307,10 +1338,14 @@ class CudaDgContext final : public DgContext {
   // and residents on the device (one K3 launch over every resident slot) before the first token.
   void fill() {
     const uint32_t G = uint32_t(x_.gated.size());
-    std::vector<std::pair<uint32_t, uint32_t>> res, pin;  // (g, unit)
+    std::vector<std::pair<uint32_t, uint32_t>> res, pin, from_store;  // (g, unit)
     for (uint32_t g = 0; g < G; ++g)
-      for (uint32_t u = 0; u < core_->units(g); ++u)
-        (core_->slot_of(core_->key(g, u)) >= 0 ? res : pin).push_back({g, u});
+      for (uint32_t u = 0; u < core_->units(g); ++u) {
+        const uint32_t k = core_->key(g, u);
+        const bool owned = peer_ && peer_->owned(k);  // an owned unit's block is never read: not filled
+        if (core_->slot_of(k) >= 0) (owned ? from_store : res).push_back({g, u});
+        else if (!owned) pin.push_back({g, u});
+      }
     const bool verify = o_.verify_hash != 0;
     unsigned nthreads = std::max(1u, std::min(16u, std::thread::hardware_concurrency()));
     std::atomic<size_t> next{0};
@@ -1375,6 +1410,17 @@ class CudaDgContext final : public DgContext {
       throw;
     }
     for (char* s : stage) cudaFreeHost(s);
+    // owned residents from their stores (the stores were checked against the hashes when they were filled)
+    for (const auto& [g, u] : from_store) {
+      const uint32_t k = core_->key(g, u);
+      const char* src = peer_->src(k, x_.unit_bytes);
+      for (size_t p = 0; p < x_.part_bytes.size(); ++p)
+        ck(cudaMemcpyAsync(unit_part_dst(core_->slot_of(k), uint32_t(p)), src + x_.part_offset[p],
+                           size_t(x_.part_bytes[p]), cudaMemcpyDefault, fs),
+           "cudaMemcpyAsync (fill from store)");
+    }
+    ck(cudaStreamSynchronize(fs), "cudaStreamSynchronize (fill from store)");
+    res.insert(res.end(), from_store.begin(), from_store.end());
     if (verify && !res.empty() && hash_of(0, 0)) verify_residents(res);
   }
 
@@ -1410,6 +1456,9 @@ class CudaDgContext final : public DgContext {
       ck_launch(dev::launch_xxh64(du, uint32_t(n), de, dout, nullptr, dmis, s), "xxh64 kernel");
       ck(cudaMemcpyAsync(&mism, dmis, 4, cudaMemcpyDeviceToHost, s), "verify result");
       ck(cudaStreamSynchronize(s), "verify sync");
+      uint32_t timeouts = 0;
+      ck(cudaError_t(dev::xxh64_take_timeouts(&timeouts)), "verify timeout word");
+      require(!timeouts, SS_E_BACKEND, "device-gated: a staging copy of the xxh64 kernel did not complete");
     } catch (...) {
       cudaFree(buf);
       throw;
@@ -1440,6 +1489,7 @@ class CudaDgContext final : public DgContext {
 
   Desc d_;
   ss_options o_;
+  std::unique_ptr<PeerTier> peer_;  // the peer tier's owners and store addresses (null: pinned RAM only)
   Layout x_;
   int device_ = 0;
   std::vector<std::unique_ptr<SourceFile>> files_;
@@ -1468,10 +1518,10 @@ class CudaDgContext final : public DgContext {
 
 }  // namespace
 
-std::unique_ptr<DgContext> open_dg_context(const Desc& d, const Plan& p, const ss_options& o) {
+std::unique_ptr<DgContext> open_dg_context(const Desc& d, const Plan& p, const ss_options& o, const PeerTier* peer) {
   require(o.backend == SS_BACKEND_CUDA, SS_E_UNSUPPORTED,
           "device-gated: this build has the CUDA backend only (ss_options.backend = SS_BACKEND_CUDA)");
-  return std::make_unique<CudaDgContext>(d, p, o);
+  return std::make_unique<CudaDgContext>(d, p, o, peer);
 }
 
 }  // namespace tsb

@@ -27,10 +27,10 @@ class HostMover final : public Mover {
   uint8_t* block_ptr(int32_t b) { return b < 0 ? stage_.data() : blocks_.data() + size_t(b) * unit_; }
   uint32_t parts() const override { return uint32_t(parts_.size()); }
   uint64_t part_bytes(uint32_t p) const override { return parts_[p]; }
-  void h2d(Stream, int32_t slot, int32_t block) override {
+  void h2d(Stream, int32_t slot, int32_t block, uint32_t) override {
     if (move_) std::memcpy(slot_ptr(slot), block_ptr(block), unit_);
   }
-  void d2h(Stream, int32_t slot, int32_t block, int32_t p) override {
+  void d2h(Stream, int32_t slot, int32_t block, int32_t p, uint32_t) override {
     if (!move_) return;
     uint64_t off = 0;
     for (uint32_t i = 0; i < parts_.size(); ++i) {
@@ -45,7 +45,7 @@ class HostMover final : public Mover {
       for (size_t i = 0; i < moves.size(); ++i)
         if (wave[i] == w && move_) std::memmove(slot_ptr(moves[i].second), slot_ptr(moves[i].first), unit_);
   }
-  void h2h(int32_t src, int32_t dst) override {
+  void h2h(int32_t src, int32_t dst, uint32_t) override {
     if (move_) std::memmove(block_ptr(dst), block_ptr(src), unit_);
   }
   void publish(Stream, uint32_t key, int32_t v) override { table_[key] = v; }

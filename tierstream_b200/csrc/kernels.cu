@@ -94,16 +94,68 @@ __global__ __launch_bounds__(kCopyThreads) void batch_kernel(const __grid_consta
 }
 
 // ---------------------------------------------------------------------------------------------------------------
-// K3: xxh64 of whole units. One lane quad per unit: lane l carries accumulator l. A warp serves 8 units and stages
-// their bytes through shared memory with cp.async (8 stages x 1 KiB per unit), so the serial lane chains never wait
-// on HBM. Units whose spans are not 32-byte multiples (except the last) or not 16-byte aligned take a one-lane path.
+// K3: xxh64 of whole units. XXH64 is four serial lane chains per unit (one 64-bit multiply-rotate-multiply per 32-byte
+// stripe and lane), so a unit's rate is set by that chain's latency and the kernel's job is to keep the chain fed and
+// run many chains at once. A CTA is one warp serving 16 units: thread t carries accumulator (t & 3) of units t >> 2
+// and (t >> 2) + 8, two independent chains interleaved. Bytes are staged in shared memory by TMA bulk copies (one
+// cp.async.bulk per unit and chunk, issued by the unit's own lane, completing on the chunk's mbarrier) through a
+// ring of 4 x 2 KiB stages per unit; unit buffers are offset by 32 B in rotation so a quad's 32-byte reads of eight
+// units spread over the banks. Units whose spans are not 16-byte aligned, or not 32-byte multiples except the last,
+// take a one-lane path from global memory. Every mbarrier wait is bounded (2 s of globaltimer, or an iteration cap);
+// one that runs out counts in g_xxh64_timeouts, marks the CTA's units as mismatches and returns after a bounded wait
+// for the copies it already issued.
 // ---------------------------------------------------------------------------------------------------------------
 constexpr uint64_t X1 = 0x9E3779B185EBCA87ULL, X2 = 0xC2B2AE3D27D4EB4FULL, X3 = 0x165667B19E3779F9ULL,
                    X4 = 0x85EBCA77C2B2AE63ULL, X5 = 0x27D4EB2F165667C5ULL;
-constexpr int kHashUnits = 8, kHashStages = 8, kHashChunk = 1024;
+constexpr int kHashUnits = 16, kHashStages = 4, kHashChunk = 2048;
+constexpr int kHashRegion = kHashStages * kHashChunk + 128;  // one unit's ring, plus room for the bank offset
+constexpr size_t kHashSmem = size_t(kHashUnits) * kHashRegion + kHashStages * 8;
+constexpr unsigned long long kWaitNs = 2000000000ull;
+
+__device__ uint32_t g_xxh64_timeouts;
 
 __device__ __forceinline__ uint64_t rotl64(uint64_t v, uint32_t r) { return (v << r) | (v >> (64 - r)); }
 __device__ __forceinline__ uint64_t lane_step(uint64_t acc, uint64_t w) { return rotl64(acc + w * X2, 31) * X1; }
+
+__device__ __forceinline__ unsigned long long globaltimer_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+__device__ __forceinline__ uint32_t smem_addr(const void* p) { return uint32_t(__cvta_generic_to_shared(p)); }
+__device__ __forceinline__ void mbar_init(uint64_t* b, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(b)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* b, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(b)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* b, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_addr(b)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded: true when the phase completed, false after kWaitNs or the iteration cap.
+__device__ bool mbar_wait(uint64_t* b, uint32_t parity) {
+  if (mbar_try_wait(b, parity)) return true;
+  const unsigned long long t0 = globaltimer_ns();
+  for (uint32_t it = 0; it < (1u << 24); ++it) {
+    if (mbar_try_wait(b, parity)) return true;
+    if ((it & 63u) == 0 && globaltimer_ns() - t0 > kWaitNs) return false;
+  }
+  return false;
+}
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_addr(dst)),
+               "l"(src), "r"(bytes), "r"(smem_addr(bar))
+               : "memory");
+}
 
 // The byte at stream position p of a unit (spans back to back).
 __device__ __forceinline__ uint8_t unit_byte(const HashUnit& u, uint64_t p) {
@@ -146,104 +198,153 @@ __device__ uint64_t finish_hash(const HashUnit& u, const uint64_t v[4], uint64_t
   return h;
 }
 
-__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
-  const uint32_t s = uint32_t(__cvta_generic_to_shared(smem));
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(s), "l"(gmem) : "memory");
+__device__ __forceinline__ uint64_t seed_acc(uint32_t l) {  // seed 0
+  return l == 0 ? X1 + X2 : l == 1 ? X2 : l == 2 ? 0 : uint64_t(0) - X1;
 }
 
 __global__ __launch_bounds__(32) void xxh64_kernel(const HashUnit* __restrict__ units, uint32_t n,
                                                    const uint64_t* __restrict__ expect, uint64_t* __restrict__ out,
                                                    uint32_t* __restrict__ bad, uint32_t* __restrict__ mismatches) {
-  extern __shared__ __align__(16) uint8_t stage_buf[];  // [kHashUnits][kHashStages][kHashChunk]
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + size_t(kHashUnits) * kHashRegion);
   const uint32_t lane = threadIdx.x, q = lane >> 2, l = lane & 3;
   const uint32_t first = blockIdx.x * kHashUnits;
-  // per unit of this warp: its stripe bytes (0 for the one-lane path) and total bytes
-  uint64_t body[kHashUnits], total[kHashUnits];
-  bool fast[kHashUnits];
-  uint32_t nchunks = 0;
+  // lane i < 16 holds unit first + i: its spans, whether it takes the staged path, its staged (stripe) bytes
+  HashUnit mine{};
+  uint64_t body = 0, total = 0;
+  if (lane < kHashUnits && first + lane < n) {
+    mine = units[first + lane];
+    bool ok = mine.n_spans >= 1 && mine.n_spans <= 4;
 #pragma unroll
-  for (int i = 0; i < kHashUnits; ++i) {
-    body[i] = total[i] = 0;
-    fast[i] = false;
-    if (first + i >= n) continue;
-    const HashUnit& u = units[first + i];
-    bool ok = u.n_spans >= 1 && u.n_spans <= 4;
-    uint64_t t = 0;
-    for (uint32_t s = 0; ok && s < u.n_spans; ++s) {
-      ok = (reinterpret_cast<uintptr_t>(u.span[s]) & 15u) == 0 && (s + 1 == u.n_spans || u.bytes[s] % 32 == 0);
-      t += u.bytes[s];
+    for (uint32_t s = 0; s < 4; ++s) {
+      if (s >= mine.n_spans) break;
+      ok = ok && (reinterpret_cast<uintptr_t>(mine.span[s]) & 15u) == 0 &&
+           (s + 1 == mine.n_spans || mine.bytes[s] % 32 == 0);
+      total += mine.bytes[s];
     }
-    if (!ok) {
-      t = 0;
-      for (uint32_t s = 0; s < u.n_spans && s < 4; ++s) t += u.bytes[s];
-    }
-    total[i] = t;
-    fast[i] = ok;
-    body[i] = ok ? t / 32 * 32 : 0;
-    const uint32_t c = uint32_t((body[i] + kHashChunk - 1) / kHashChunk);
-    nchunks = c > nchunks ? c : nchunks;
+    body = ok ? total / 32 * 32 : 0;
   }
-  // issue chunk c of every unit: 8 units x 64 vectors, 16 per lane
+  const uint32_t my_chunks = uint32_t((body + kHashChunk - 1) / kHashChunk);
+  const uint32_t nchunks = __reduce_max_sync(0xffffffffu, my_chunks);
+  // the two units this thread hashes: q and q + 8
+  const uint64_t body0 = __shfl_sync(0xffffffffu, body, int(q)), body1 = __shfl_sync(0xffffffffu, body, int(q + 8));
+  uint8_t* region = smem + size_t(lane) * kHashRegion + (lane & 3u) * 32;  // valid for lane < 16
+  const uint8_t* rd0 = smem + size_t(q) * kHashRegion + (q & 3u) * 32 + 8 * l;
+  const uint8_t* rd1 = smem + size_t(q + 8) * kHashRegion + ((q + 8) & 3u) * 32 + 8 * l;
+  if (lane == 0) {
+    for (int s = 0; s < kHashStages; ++s) mbar_init(bars + s, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncwarp();
+  // chunk c of every unit into stage c % kHashStages: lane 0 arms the stage's barrier with the chunk's bytes, each
+  // unit's lane issues its copies (one per span the chunk touches)
   auto issue = [&](uint32_t c) {
-    const size_t stage_off = size_t(c % kHashStages) * kHashChunk;
-#pragma unroll 4
-    for (uint32_t e = lane; e < kHashUnits * (kHashChunk / 16); e += 32) {
-      const uint32_t i = e / (kHashChunk / 16), v = e % (kHashChunk / 16);
-      uint64_t p = uint64_t(c) * kHashChunk + uint64_t(v) * 16;
-      if (p >= body[i]) continue;
-      const HashUnit& u = units[first + i];
-      uint32_t s = 0;
-      while (p >= u.bytes[s]) {
-        p -= u.bytes[s];
-        ++s;
-      }
-      cp_async16(stage_buf + size_t(i) * kHashStages * kHashChunk + stage_off + size_t(v) * 16, u.span[s] + p);
-    }
-    asm volatile("cp.async.commit_group;" ::: "memory");
-  };
-  uint64_t acc = l == 0 ? X1 + X2 : l == 1 ? X2 : l == 2 ? 0 : uint64_t(0) - X1;  // seed 0
-  for (uint32_t c = 0; c + 1 < kHashStages; ++c) {
-    if (c < nchunks) issue(c);
-    else asm volatile("cp.async.commit_group;" ::: "memory");
-  }
-  for (uint32_t c = 0; c < nchunks; ++c) {
-    if (c + kHashStages - 1 < nchunks) issue(c + kHashStages - 1);
-    else asm volatile("cp.async.commit_group;" ::: "memory");
-    asm volatile("cp.async.wait_group %0;" ::"n"(kHashStages - 1) : "memory");
-    __syncwarp();
+    uint64_t* bar = bars + (c % kHashStages);
     const uint64_t start = uint64_t(c) * kHashChunk;
-    if (start < body[q]) {
-      const uint64_t left = body[q] - start;
-      const uint32_t stripes = left >= kHashChunk ? kHashChunk / 32 : uint32_t(left / 32);
-      const uint64_t* w = reinterpret_cast<const uint64_t*>(stage_buf + size_t(q) * kHashStages * kHashChunk +
-                                                            size_t(c % kHashStages) * kHashChunk) + l;
-#pragma unroll 8
-      for (uint32_t s = 0; s < stripes; ++s) acc = lane_step(acc, w[4 * s]);
-    }
+    const uint32_t bytes = start < body ? uint32_t(body - start < kHashChunk ? body - start : kHashChunk) : 0u;
+    const uint32_t all = __reduce_add_sync(0xffffffffu, bytes);
+    if (lane == 0) mbar_arrive_expect_tx(bar, all);
     __syncwarp();
-  }
-  asm volatile("cp.async.wait_group 0;" ::: "memory");
-  // gather the quad's accumulators on its lane 0
-  uint64_t v[4];
+    if (!bytes) return;
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // the stage was last read by ordinary loads
+    uint8_t* dst = region + size_t(c % kHashStages) * kHashChunk;
+    uint64_t p = start;
+    uint32_t left = bytes;
 #pragma unroll
-  for (int k = 0; k < 4; ++k) v[k] = __shfl_sync(0xffffffffu, acc, int((lane & ~3u) + k));
-  const uint32_t idx = first + q;
-  if (l != 0 || idx >= n) return;
-  const HashUnit& u = units[idx];
-  uint64_t h;
-  if (fast[q]) {
-    h = finish_hash(u, v, total[q], body[q]);
-  } else {  // one lane: the stripes from global memory
-    uint64_t a[4] = {X1 + X2, X2, 0, uint64_t(0) - X1};
-    const uint64_t b = total[q] / 32 * 32;
-    for (uint64_t p = 0; p < b; p += 32)
-      for (int k = 0; k < 4; ++k) a[k] = lane_step(a[k], unit_le64(u, p + 8 * uint64_t(k)));
-    h = finish_hash(u, a, total[q], b);
+    for (uint32_t s = 0; s < 4; ++s) {
+      if (s >= mine.n_spans || !left) break;
+      if (p >= mine.bytes[s]) {
+        p -= mine.bytes[s];
+        continue;
+      }
+      const uint64_t avail = mine.bytes[s] - p;
+      const uint32_t take = avail < left ? uint32_t(avail) : left;
+      bulk_load(dst, mine.span[s] + p, take, bar);
+      dst += take;
+      left -= take;
+      p = 0;
+    }
+  };
+  for (uint32_t c = 0; c < kHashStages && c < nchunks; ++c) issue(c);
+  uint64_t a0 = seed_acc(l), a1 = seed_acc(l);
+  bool timed_out = false;
+  uint32_t c = 0;
+  for (; c < nchunks; ++c) {
+    const bool ok = mbar_wait(bars + (c % kHashStages), (c / kHashStages) & 1u);
+    if (!__all_sync(0xffffffffu, ok)) {
+      timed_out = true;
+      break;
+    }
+    const size_t so = size_t(c % kHashStages) * kHashChunk;
+    const uint64_t* w0 = reinterpret_cast<const uint64_t*>(rd0 + so);
+    const uint64_t* w1 = reinterpret_cast<const uint64_t*>(rd1 + so);
+    const uint64_t start = uint64_t(c) * kHashChunk;
+    const uint32_t n0 = start < body0 ? uint32_t((body0 - start < kHashChunk ? body0 - start : kHashChunk) / 32) : 0u;
+    const uint32_t n1 = start < body1 ? uint32_t((body1 - start < kHashChunk ? body1 - start : kHashChunk) / 32) : 0u;
+    // batches of 8 stripes: the loads and the w * X2 products (off the chains) first, then the two chains' steps
+    // interleaved, so each step waits only on its own chain
+    const uint32_t both = n0 < n1 ? n0 : n1;
+    uint32_t s = 0;
+    for (; s + 8 <= both; s += 8) {
+      uint64_t p0[8], p1[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        p0[k] = w0[4 * (s + k)] * X2;
+        p1[k] = w1[4 * (s + k)] * X2;
+      }
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        a0 = rotl64(a0 + p0[k], 31) * X1;
+        a1 = rotl64(a1 + p1[k], 31) * X1;
+      }
+    }
+    for (uint32_t t = s; t < n0; ++t) a0 = lane_step(a0, w0[4 * t]);
+    for (uint32_t t = s; t < n1; ++t) a1 = lane_step(a1, w1[4 * t]);
+    __syncwarp();  // every lane is done with the stage before it is refilled
+    if (c + kHashStages < nchunks) issue(c + kHashStages);
   }
-  out[idx] = h;
-  if (expect && expect[idx] != h) {
-    if (bad) bad[idx] = 1;
-    if (mismatches) atomicAdd(mismatches, 1u);
+  if (timed_out) {
+    if (lane == 0) atomicAdd(&g_xxh64_timeouts, 1u);
+    // the copies already issued (stages c .. c + kHashStages - 1) land before the CTA leaves, each wait bounded
+    for (uint32_t k = c; k < nchunks && k < c + kHashStages; ++k)
+      (void)mbar_wait(bars + (k % kHashStages), (k / kHashStages) & 1u);
+    if (lane < kHashUnits && first + lane < n) {
+      out[first + lane] = 0;
+      if (bad) bad[first + lane] = 1;
+      if (expect && mismatches) atomicAdd(mismatches, 1u);
+    }
+    return;
+  }
+  // gather each quad's accumulators on its lane 0, then finish units q and q + 8 there
+  uint64_t v0[4], v1[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    v0[k] = __shfl_sync(0xffffffffu, a0, int((lane & ~3u) + k));
+    v1[k] = __shfl_sync(0xffffffffu, a1, int((lane & ~3u) + k));
+  }
+  if (l != 0) return;
+  for (int which = 0; which < 2; ++which) {
+    const uint32_t idx = first + q + 8u * uint32_t(which);
+    if (idx >= n) continue;
+    const HashUnit& u = units[idx];
+    const uint64_t b = which ? body1 : body0;
+    uint64_t t = 0;
+    for (uint32_t s = 0; s < u.n_spans && s < 4; ++s) t += u.bytes[s];
+    uint64_t h;
+    if (b) {
+      h = finish_hash(u, which ? v1 : v0, t, b);
+    } else {  // shorter than a stripe, or the one-lane path from global memory
+      uint64_t a[4] = {seed_acc(0), seed_acc(1), seed_acc(2), seed_acc(3)};
+      const uint64_t bb = t / 32 * 32;
+      for (uint64_t p = 0; p < bb; p += 32)
+        for (int k = 0; k < 4; ++k) a[k] = lane_step(a[k], unit_le64(u, p + 8 * uint64_t(k)));
+      h = finish_hash(u, a, t, bb);
+    }
+    out[idx] = h;
+    if (expect && expect[idx] != h) {
+      if (bad) bad[idx] = 1;
+      if (mismatches) atomicAdd(mismatches, 1u);
+    }
   }
 }
 
@@ -391,16 +492,16 @@ int launch_batch(const Batch& b, int blocks, void* stream) {
 int launch_xxh64(const HashUnit* units_dev, uint32_t n, const uint64_t* expect_dev, uint64_t* out_dev,
                  uint32_t* bad_dev, uint32_t* mismatches_dev, void* stream) {
   if (!n) return 0;
-  const size_t smem = size_t(kHashUnits) * kHashStages * kHashChunk;
   static bool attr = false;
   if (!attr) {
-    const cudaError_t e = cudaFuncSetAttribute(xxh64_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+    const cudaError_t e =
+        cudaFuncSetAttribute(xxh64_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kHashSmem));
     if (e != cudaSuccess) return int(e);
     attr = true;
   }
   const uint32_t blocks = (n + kHashUnits - 1) / kHashUnits;
-  xxh64_kernel<<<blocks, 32, smem, static_cast<cudaStream_t>(stream)>>>(units_dev, n, expect_dev, out_dev, bad_dev,
-                                                                        mismatches_dev);
+  xxh64_kernel<<<blocks, 32, kHashSmem, static_cast<cudaStream_t>(stream)>>>(units_dev, n, expect_dev, out_dev,
+                                                                             bad_dev, mismatches_dev);
   return last_error();
 }
 
@@ -434,8 +535,18 @@ int preload() {
     const cudaError_t e = cudaFuncGetAttributes(&a, f);
     if (e != cudaSuccess) return int(e);
   }
-  const size_t smem = size_t(kHashUnits) * kHashStages * kHashChunk;
-  return int(cudaFuncSetAttribute(xxh64_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
+  return int(cudaFuncSetAttribute(xxh64_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kHashSmem)));
+}
+
+int xxh64_take_timeouts(uint32_t* out) {
+  uint32_t v = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&v, g_xxh64_timeouts, sizeof v);
+  if (e == cudaSuccess && v) {
+    const uint32_t zero = 0;
+    e = cudaMemcpyToSymbol(g_xxh64_timeouts, &zero, sizeof zero);
+  }
+  *out = v;
+  return int(e);
 }
 
 }  // namespace dev

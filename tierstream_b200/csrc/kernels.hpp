@@ -43,6 +43,9 @@ struct HashUnit {
 };
 int launch_xxh64(const HashUnit* units_dev, uint32_t n, const uint64_t* expect_dev, uint64_t* out_dev,
                  uint32_t* bad_dev, uint32_t* mismatches_dev, void* stream);
+// Staging waits of the xxh64 kernel that ran out since the last call (their units were reported as mismatches and
+// hashed as 0), then reset; synchronous. Non-zero means the device did not complete a bulk copy in 2 s.
+int xxh64_take_timeouts(uint32_t* out);
 
 // ---- K2: device-gated decode control kernels ----
 // The record an export writes for the service (mapped host memory); the layout is the reference's DgRecord

@@ -1,0 +1,247 @@
+// The peer tier's planner and stores (peer.hpp).
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <atomic>
+#include <chrono>
+#include <cstring>
+#include <memory>
+#include <mutex>
+#include <numeric>
+#include <string>
+#include <thread>
+
+#include "errors.hpp"
+#include "kernels.hpp"
+#include "peer.hpp"
+#include "source_file.hpp"
+
+namespace tsb {
+namespace {
+
+void ck(cudaError_t e, const char* what) {
+  if (e != cudaSuccess) {
+    (void)cudaGetLastError();
+    fail(SS_E_BACKEND, std::string(what) + ": " + cudaGetErrorString(e));
+  }
+}
+
+}  // namespace
+
+GatedKeys gated_keys(const Desc& d) {
+  GatedKeys g;
+  g.base.push_back(0);
+  uint64_t keys = 0;
+  for (size_t L = 0; L < d.layers.size(); ++L) {
+    const Layer& l = d.layers[L];
+    if (l.n_units == 0) continue;
+    require(l.streamable, SS_E_UNSUPPORTED,
+            "peer tier: layer " + std::to_string(l.index) + " has non-streamable units (every unit is gated)");
+    if (!g.unit_bytes) g.unit_bytes = l.unit_bytes;
+    require(l.unit_bytes == g.unit_bytes, SS_E_UNSUPPORTED, "peer tier: gated layers of different unit sizes");
+    g.layers.push_back(int(L));
+    keys += uint64_t(l.n_units);
+    require(keys < 0x7fffffffull, SS_E_INVALID, "peer tier: more than 2^31 - 1 gated units");
+    g.base.push_back(uint32_t(keys));
+  }
+  require(!g.layers.empty(), SS_E_INVALID, "peer tier: the descriptor has no streamable units");
+  return g;
+}
+
+std::vector<int32_t> plan_owners(const uint64_t* counts, uint32_t keys, uint32_t world, const uint64_t* cap_units) {
+  require(world >= 1 && world <= 1024, SS_E_INVALID, "tsb_peer_plan: world must be 1..1024");
+  require(counts != nullptr || keys == 0, SS_E_INVALID, "tsb_peer_plan: null counts");
+  std::vector<uint32_t> order(keys);
+  std::iota(order.begin(), order.end(), 0u);
+  std::stable_sort(order.begin(), order.end(), [&](uint32_t a, uint32_t b) { return counts[a] > counts[b]; });
+  std::vector<uint64_t> load(world, 0), units(world, 0);
+  std::vector<int32_t> owner(keys, -1);
+  for (uint32_t k : order) {
+    int32_t best = -1;
+    for (uint32_t r = 0; r < world; ++r) {
+      if (cap_units && units[r] >= cap_units[r]) continue;
+      if (best < 0 || load[r] < load[size_t(best)] ||
+          (load[r] == load[size_t(best)] && units[r] < units[size_t(best)]))
+        best = int32_t(r);
+    }
+    if (best < 0) continue;
+    owner[k] = best;
+    load[size_t(best)] += counts[k];
+    ++units[size_t(best)];
+  }
+  return owner;
+}
+
+std::vector<int64_t> store_index(const std::vector<int32_t>& owner, uint32_t world, std::vector<uint64_t>* per_rank) {
+  std::vector<uint64_t> n(world, 0);
+  std::vector<int64_t> index(owner.size(), -1);
+  for (size_t k = 0; k < owner.size(); ++k) {
+    const int32_t o = owner[k];
+    if (o < 0) continue;
+    require(uint32_t(o) < world, SS_E_INVALID, "peer tier: owner " + std::to_string(o) + " of key " +
+                                                   std::to_string(k) + " is not a rank below the world size");
+    index[k] = int64_t(n[size_t(o)]++);
+  }
+  if (per_rank) *per_rank = n;
+  return index;
+}
+
+PeerStore::PeerStore(const Desc& d, const std::vector<int32_t>& owner, int32_t rank, int device, bool verify)
+    : device_(device) {
+  const auto t0 = std::chrono::steady_clock::now();
+  const GatedKeys gk = gated_keys(d);
+  require(owner.size() == gk.keys(), SS_E_INVALID,
+          "peer tier: the owner map has " + std::to_string(owner.size()) + " keys, the descriptor " +
+              std::to_string(gk.keys()));
+  require(rank >= 0, SS_E_INVALID, "peer tier: negative rank");
+  std::vector<std::pair<uint32_t, uint32_t>> mine;  // (gated ordinal, unit), key order
+  for (uint32_t g = 0; g + 1 < gk.base.size(); ++g)
+    for (uint32_t u = 0; u < gk.base[g + 1] - gk.base[g]; ++u)
+      if (owner[gk.base[g] + u] == rank) mine.push_back({g, u});
+  units_ = mine.size();
+  bytes_ = units_ * gk.unit_bytes;
+  ck(cudaSetDevice(device), "cudaSetDevice (peer store)");
+  if (!bytes_) return;
+  ck(cudaMalloc(reinterpret_cast<void**>(&base_), size_t(bytes_)), "cudaMalloc (peer store)");
+  try {
+    std::vector<std::unique_ptr<SourceFile>> files;
+    for (const Source& s : d.sources) files.push_back(std::make_unique<SourceFile>(s.path, s.align, false));
+    auto read_unit = [&](uint32_t g, uint32_t u, char* dst) {
+      const Layer& l = d.layers[size_t(gk.layers[g])];
+      uint64_t off = 0;
+      for (const Part& p : l.parts) {
+        files[size_t(p.source)]->read(dst + off, p.offset + uint64_t(u) * p.stride, p.bytes);
+        off += p.bytes;
+      }
+    };
+    // a ring of pinned staging units, one reader thread each; copies on one stream, the ring reused after a sync
+    const unsigned nthreads = std::max(1u, std::min(16u, std::thread::hardware_concurrency()));
+    const size_t ring = std::min<size_t>(units_, nthreads);
+    std::vector<char*> stage(ring, nullptr);
+    cudaStream_t s = nullptr;
+    auto release = [&] {
+      for (char* p : stage)
+        if (p) cudaFreeHost(p);
+      if (s) cudaStreamDestroy(s);
+    };
+    try {
+      for (auto& p : stage)
+        ck(cudaHostAlloc(reinterpret_cast<void**>(&p), size_t(gk.unit_bytes), cudaHostAllocPortable),
+           "cudaHostAlloc (peer store staging)");
+      ck(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking), "cudaStreamCreate (peer store)");
+      std::mutex err_mu;
+      std::string err;
+      for (size_t first = 0; first < units_; first += ring) {
+        const size_t n = std::min(ring, size_t(units_) - first);
+        std::vector<std::thread> th;
+        for (size_t i = 0; i < n; ++i)
+          th.emplace_back([&, i] {
+            try {
+              read_unit(mine[first + i].first, mine[first + i].second, stage[i]);
+            } catch (const std::exception& e) {
+              std::lock_guard<std::mutex> lk(err_mu);
+              if (err.empty()) err = e.what();
+            }
+          });
+        for (auto& t : th) t.join();
+        if (!err.empty()) fail(SS_E_IO, "peer tier: " + err);
+        for (size_t i = 0; i < n; ++i)
+          ck(cudaMemcpyAsync(base_ + (first + i) * gk.unit_bytes, stage[i], size_t(gk.unit_bytes),
+                             cudaMemcpyHostToDevice, s),
+             "cudaMemcpyAsync (peer store fill)");
+        ck(cudaStreamSynchronize(s), "cudaStreamSynchronize (peer store fill)");
+      }
+      // the store against the descriptor's hashes: K3 over every unit, in launches of up to 4096 units
+      const bool hashes = !d.layers[size_t(gk.layers[0])].hash.empty();
+      if (verify && hashes) {
+        const size_t chunk = 4096;
+        void* buf = nullptr;
+        const size_t nb = std::min<size_t>(chunk, units_);
+        ck(cudaMalloc(&buf, nb * (sizeof(dev::HashUnit) + 16) + 16), "cudaMalloc (peer store verify)");
+        auto* du = static_cast<dev::HashUnit*>(buf);
+        auto* de = reinterpret_cast<uint64_t*>(du + nb);
+        auto* dout = de + nb;
+        auto* dmis = reinterpret_cast<uint32_t*>(dout + nb);
+        uint32_t mism = 0;
+        try {
+          ck(cudaMemsetAsync(dmis, 0, 4, s), "peer store verify clear");
+          for (size_t first = 0; first < units_; first += chunk) {
+            const size_t n = std::min(chunk, size_t(units_) - first);
+            std::vector<dev::HashUnit> hu(n);
+            std::vector<uint64_t> want(n);
+            for (size_t i = 0; i < n; ++i) {
+              const auto [g, u] = mine[first + i];
+              const Layer& l = d.layers[size_t(gk.layers[g])];
+              hu[i] = dev::HashUnit{};
+              hu[i].n_spans = 1;
+              hu[i].span[0] = reinterpret_cast<const uint8_t*>(base_ + (first + i) * gk.unit_bytes);
+              hu[i].bytes[0] = gk.unit_bytes;
+              want[i] = l.hash[u];
+            }
+            ck(cudaMemcpyAsync(du, hu.data(), n * sizeof(dev::HashUnit), cudaMemcpyHostToDevice, s), "verify upload");
+            ck(cudaMemcpyAsync(de, want.data(), n * 8, cudaMemcpyHostToDevice, s), "verify upload");
+            ck(cudaError_t(dev::launch_xxh64(du, uint32_t(n), de, dout, nullptr, dmis, s)), "xxh64 kernel");
+            ck(cudaStreamSynchronize(s), "peer store verify");  // the host tables are reused
+          }
+          ck(cudaMemcpy(&mism, dmis, 4, cudaMemcpyDeviceToHost), "peer store verify result");
+          uint32_t timeouts = 0;
+          ck(cudaError_t(dev::xxh64_take_timeouts(&timeouts)), "peer store verify timeout word");
+          require(!timeouts, SS_E_BACKEND, "peer tier: a staging copy of the xxh64 kernel did not complete");
+        } catch (...) {
+          cudaFree(buf);
+          throw;
+        }
+        cudaFree(buf);
+        require(mism == 0, SS_E_HASH,
+                "peer tier: " + std::to_string(mism) + " stored unit(s) differ from their descriptor hashes");
+      }
+    } catch (...) {
+      release();
+      throw;
+    }
+    release();
+  } catch (...) {
+    cudaFree(base_);
+    base_ = nullptr;
+    throw;
+  }
+  fill_s_ = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+}
+
+void ipc_export(const void* base, void* handle) {
+  require(base && handle, SS_E_INVALID, "tsb_peer_store_export: an empty store has no handle");
+  static_assert(sizeof(cudaIpcMemHandle_t) == 64, "a CUDA IPC handle is 64 bytes");
+  cudaIpcMemHandle_t h;
+  ck(cudaIpcGetMemHandle(&h, const_cast<void*>(base)), "cudaIpcGetMemHandle (peer store)");
+  std::memcpy(handle, &h, sizeof h);
+}
+
+void* ipc_map(const void* handle, int device) {
+  require(handle != nullptr, SS_E_INVALID, "tsb_peer_map: null handle");
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof h);
+  int cur = 0;
+  ck(cudaGetDevice(&cur), "cudaGetDevice");
+  ck(cudaSetDevice(device), "cudaSetDevice (peer map)");
+  void* p = nullptr;
+  const cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+  cudaSetDevice(cur);
+  ck(e, "cudaIpcOpenMemHandle (peer store)");
+  return p;
+}
+
+void ipc_unmap(void* base) {
+  if (base) ck(cudaIpcCloseMemHandle(base), "cudaIpcCloseMemHandle (peer store)");
+}
+
+PeerStore::~PeerStore() {
+  if (base_) {
+    int cur = 0;
+    cudaGetDevice(&cur);
+    cudaSetDevice(device_);
+    cudaFree(base_);
+    cudaSetDevice(cur);
+  }
+}
+
+}  // namespace tsb

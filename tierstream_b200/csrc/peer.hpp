@@ -1,0 +1,79 @@
+// The peer tier: gated units partitioned over the GPUs' HBM. Each GPU keeps the units it owns in a store (one device
+// allocation, unit-major: unit i of the store at base + i * unit_bytes, its parts back to back in descriptor order); a
+// device-gated miss on an owned unit is copied from its owner's store (over NVLink for a peer, inside HBM for the
+// GPU's own) instead of from pinned RAM. The slot cache's decisions do not change: an owned unit keeps its Host home
+// and its block number; only the source of its bytes does. When every unit is owned, no pinned block is allocated
+// (blocks are bookkeeping only) and write-backs move no bytes, since every unit's bytes live in a store.
+//
+// There is no counterpart in the reference (it declares SS_TIER_PAIR, ss.h:103, and never fetches from it).
+#pragma once
+
+#include <cstdint>
+#include <memory>
+#include <vector>
+
+#include "desc.hpp"
+
+namespace tsb {
+
+// Gated layers in ordinal order (layers with units, every one streamable) and the unit base of each (G + 1 entries):
+// the key space the device-gated context and the peer tier share.
+struct GatedKeys {
+  std::vector<int> layers;
+  std::vector<uint32_t> base;
+  uint64_t unit_bytes = 0;
+  uint32_t keys() const { return base.empty() ? 0 : base.back(); }
+};
+GatedKeys gated_keys(const Desc& d);
+
+// The owner of every key, by routing counts summed over the ranks: keys in descending count (ties: lower key first),
+// each to the rank with the least count assigned so far (ties: fewer units, then the lower rank) among those below
+// their unit capacity; -1 when every rank is full (the key stays in pinned RAM). Deterministic: every rank that
+// plans from the same counts gets the same owners.
+std::vector<int32_t> plan_owners(const uint64_t* counts, uint32_t keys, uint32_t world, const uint64_t* cap_units);
+
+// index[k]: the position of key k in its owner's store (keys of one owner in key order); -1 for unowned keys.
+std::vector<int64_t> store_index(const std::vector<int32_t>& owner, uint32_t world, std::vector<uint64_t>* per_rank);
+
+struct PeerTier {
+  uint32_t world = 0;
+  int32_t rank = -1;
+  std::vector<int32_t> owner;   // per gated key
+  std::vector<int64_t> index;   // per gated key
+  std::vector<char*> base;      // per rank: its store's device address in this process
+  bool all_owned = false;
+  int copy = 0;                 // 0 = land kernel, 1 = copy engines
+  const char* src(uint32_t key, uint64_t unit_bytes) const {
+    return base[size_t(owner[key])] + uint64_t(index[key]) * unit_bytes;
+  }
+  bool owned(uint32_t key) const { return owner[key] >= 0; }
+};
+
+// This rank's store: cudaMalloc'd on `device`, filled from the descriptor's sources, checked on the device against
+// the descriptor's hashes (K3) when verify is set and the descriptor has them.
+// CUDA IPC for the stores: the handle of a store (64 bytes), a mapping of another process's store on `device` with
+// peer access enabled, and its release.
+void ipc_export(const void* base, void* handle);
+void* ipc_map(const void* handle, int device);
+void ipc_unmap(void* base);
+
+class PeerStore {
+ public:
+  PeerStore(const Desc& d, const std::vector<int32_t>& owner, int32_t rank, int device, bool verify);
+  ~PeerStore();
+  PeerStore(const PeerStore&) = delete;
+  PeerStore& operator=(const PeerStore&) = delete;
+  char* base() const { return base_; }
+  uint64_t bytes() const { return bytes_; }
+  uint64_t units() const { return units_; }
+  int device() const { return device_; }
+  double fill_seconds() const { return fill_s_; }
+
+ private:
+  char* base_ = nullptr;
+  uint64_t bytes_ = 0, units_ = 0;
+  int device_ = 0;
+  double fill_s_ = 0;
+};
+
+}  // namespace tsb

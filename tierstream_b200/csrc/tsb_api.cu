@@ -99,6 +99,9 @@ ss_status tsb_xxh64_units(const void* const* spans, const uint64_t* span_bytes, 
                                           nullptr, mismatches_dev, s)),
        "xxh64 kernel");
     ck(cudaStreamSynchronize(s), "tsb_xxh64_units: sync");  // the host unit table is released on return
+    uint32_t timeouts = 0;
+    ck(cudaError_t(tsb::dev::xxh64_take_timeouts(&timeouts)), "tsb_xxh64_units: timeout word");
+    tsb::require(!timeouts, SS_E_BACKEND, "tsb_xxh64_units: a staging copy of the xxh64 kernel did not complete");
   });
 }
 

@@ -88,6 +88,10 @@ extern "C" ss_status tsb_xxh64_units_static(const void* const* spans, const uint
        "tsb_xxh64_units_static: unit table upload");
     ck(cudaError_t(tsb::dev::launch_xxh64(table, n, expect_dev, out_dev, nullptr, mismatches_dev, s)), "xxh64 kernel");
     ck(cudaStreamSynchronize(s), "tsb_xxh64_units_static: sync");
+    uint32_t timeouts = 0;
+    ck(cudaError_t(tsb::dev::xxh64_take_timeouts(&timeouts)), "tsb_xxh64_units_static: timeout word");
+    tsb::require(!timeouts, SS_E_BACKEND,
+                 "tsb_xxh64_units_static: a staging copy of the xxh64 kernel did not complete");
     return SS_OK;
   } catch (const tsb::Error& e) {
     tsb::set_error(e.what());

@@ -26,8 +26,9 @@ def measure(layers=32, units=8, part=256 << 10, top_k=2, tokens=200, warmup=20):
                         mode=1, slices=8)
     eng = abi.load_engine()
     try:
-        ids = synth.zipf_trace(1, layers, units, top_k, s=1.0, seed=3)[0]
-        # every routed unit resident: seed the one non-resident unit of each layer first (no miss ever after)
+        # routes only to residents (units 0 .. units - 2 of every layer): no token ever misses, so no wait kernel
+        # ever waits on the service (the run also works under a profiler that serialises kernels)
+        ids = np.tile(np.arange(top_k, dtype=np.int32), (layers, 1))
         run.ids_pin.numpy()[:] = ids.reshape(-1)
         run.ids_dev.copy_(run.ids_pin)
         for _ in range(3):

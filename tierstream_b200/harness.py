@@ -16,7 +16,7 @@ class DgRun:
     def __init__(self, model, residents_per_layer=None, resident_keys=None, spare_per_layer=1, max_ids=2,
                  host_spare_units=None, diag=False, test_hooks=True, wb_defer=1, wb_stream=1, verify=False,
                  n_pred=0, slices=64, mode=0, timeout_ms=10000, device_bytes=None, with_reader=True,
-                 resident_order=None, inclusive=0):
+                 resident_order=None, inclusive=0, peer=None):
         self.model = model
         G, U = model.layers, model.units
         self.G, self.U, self.n_ids, self.n_pred = G, U, max_ids, n_pred
@@ -54,7 +54,7 @@ class DgRun:
         o.verify_hash = 1 if verify else 0
         o.dg_wait_timeout_ms = timeout_ms
         o.dg_inclusive_blocks = inclusive
-        self.ctx = runtime.DgContext(self.desc, self.plan, o)
+        self.ctx = runtime.DgContext(self.desc, self.plan, o, peer=peer)
         self.stream = torch.cuda.Stream()
         self.ids_pin = torch.zeros(G * max_ids, dtype=torch.int32).pin_memory()
         self.ids_dev = torch.zeros(G * max_ids, dtype=torch.int32, device="cuda")

@@ -1,0 +1,157 @@
+"""The peer tier from Python (the library does the work; torch.distributed is only the plumbing between the ranks).
+
+One process per GPU. Each rank counts its own routes per gated key; the counts are summed over the ranks by one
+all-reduce (NCCL on GPUs, gloo on CPU) -- the tier's only collective; every rank then plans the same owners
+(tsb_peer_plan), fills its own store from the descriptor's sources (tsb_peer_store_create), and the ranks exchange
+their stores' CUDA IPC handles (an all-gather of 64-byte handles) and map each other's stores. A device-gated context
+opened with the resulting Tier (runtime.DgContext(..., peer=tier)) copies each miss on an owned unit from its owner's
+store: over NVLink for a peer, inside HBM for its own.
+"""
+import ctypes as C
+
+import numpy as np
+
+from . import abi
+
+
+def plan_owners(counts, world, cap_units=None):
+    """owner[keys] from routing counts already summed over the ranks (tsb_peer_plan)."""
+    counts = np.ascontiguousarray(counts, dtype=np.uint64)
+    keys = counts.size
+    owner = np.empty(keys, dtype=np.int32)
+    cap = None
+    if cap_units is not None:
+        cap = np.ascontiguousarray(np.broadcast_to(np.asarray(cap_units, dtype=np.uint64), (world,)))
+    abi.check(abi.load().tsb_peer_plan(counts.ctypes.data_as(C.POINTER(C.c_uint64)), keys, world,
+                                       cap.ctypes.data_as(C.POINTER(C.c_uint64)) if cap is not None else None,
+                                       owner.ctypes.data_as(C.POINTER(C.c_int32))))
+    return owner
+
+
+def store_index(owner, world):
+    """(index[keys], units_per_rank[world]) of an owner map (tsb_peer_index)."""
+    owner = np.ascontiguousarray(owner, dtype=np.int32)
+    index = np.empty(owner.size, dtype=np.int64)
+    per = np.empty(world, dtype=np.uint64)
+    abi.check(abi.load().tsb_peer_index(owner.ctypes.data_as(C.POINTER(C.c_int32)), owner.size, world,
+                                        index.ctypes.data_as(C.POINTER(C.c_int64)),
+                                        per.ctypes.data_as(C.POINTER(C.c_uint64))))
+    return index, per
+
+
+class Store:
+    """This rank's store: the units it owns, in its GPU's HBM (tsb_peer_store_create)."""
+
+    def __init__(self, desc, owner, rank, device=0, verify=True):
+        owner = np.ascontiguousarray(owner, dtype=np.int32)
+        self.h = C.c_void_p()
+        abi.check(abi.load().tsb_peer_store_create(desc.h, owner.ctypes.data_as(C.POINTER(C.c_int32)), owner.size,
+                                                   rank, device, 1 if verify else 0, C.byref(self.h)))
+        self.base = abi.load().tsb_peer_store_base(self.h) or 0
+        self.bytes = int(abi.load().tsb_peer_store_bytes(self.h))
+
+    def handle(self):
+        """The store's CUDA IPC handle (64 bytes), or 64 zero bytes for an empty store."""
+        if not self.base:
+            return bytes(abi.PEER_HANDLE_BYTES)
+        buf = (C.c_uint8 * abi.PEER_HANDLE_BYTES)()
+        abi.check(abi.load().tsb_peer_store_export(self.h, buf))
+        return bytes(buf)
+
+    def close(self):
+        if getattr(self, "h", None):
+            abi.load().tsb_peer_store_free(self.h)
+            self.h = None
+
+    def __del__(self):
+        self.close()
+
+
+def map_store(handle, device):
+    """Maps another process's store on `device`; returns its address here (0 for an empty store's handle)."""
+    if not any(handle):
+        return 0
+    buf = (C.c_uint8 * abi.PEER_HANDLE_BYTES).from_buffer_copy(handle)
+    base = C.c_void_p()
+    abi.check(abi.load().tsb_peer_map(buf, device, C.byref(base)))
+    return base.value or 0
+
+
+def unmap_store(base):
+    if base:
+        abi.check(abi.load().tsb_peer_unmap(C.c_void_p(base)))
+
+
+class Tier:
+    """The owners and each rank's store address as seen from this process: the tsb_peer_tier of tsb_open_peer."""
+
+    def __init__(self, world, rank, owner, bases, copy=0):
+        self.world, self.rank, self.copy = world, rank, copy
+        self.owner = np.ascontiguousarray(owner, dtype=np.int32)
+        self.bases = (C.c_void_p * world)(*[b or None for b in bases])
+
+    def struct(self):
+        t = abi.tsb_peer_tier()
+        t.struct_size = C.sizeof(t)
+        t.world, t.rank, t.keys = self.world, self.rank, self.owner.size
+        t.owner = self.owner.ctypes.data_as(C.POINTER(C.c_int32))
+        t.store_base = C.cast(self.bases, C.POINTER(C.c_void_p))
+        t.copy = self.copy
+        return t
+
+
+def all_reduce_counts(counts, dist, device=None):
+    """The tier's one collective: routing counts summed over the ranks (int64 on the GPU over NCCL, CPU over gloo)."""
+    import torch
+    t = torch.from_numpy(np.ascontiguousarray(counts, dtype=np.int64))
+    if device is not None:
+        t = t.to(device)
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return t.cpu().numpy().astype(np.uint64)
+
+
+def all_gather_handles(handle, dist, world, device=None):
+    import torch
+    mine = torch.frombuffer(bytearray(handle), dtype=torch.uint8)
+    if device is not None:
+        mine = mine.to(device)
+    out = [torch.empty_like(mine) for _ in range(world)]
+    dist.all_gather(out, mine)
+    return [bytes(o.cpu().numpy().tobytes()) for o in out]
+
+
+class PeerSetup:
+    """Everything a rank holds for the tier: its store, the mapped peer stores and the Tier to open with.
+    Close it after the context that uses it."""
+
+    def __init__(self, desc, local_counts, dist, world, rank, device, cap_units=None, verify=True, copy=0,
+                 collective_device=None):
+        if dist is None:  # one rank: nothing to exchange
+            assert world == 1 and rank == 0
+            self.counts = np.ascontiguousarray(local_counts, dtype=np.uint64)
+        else:
+            self.counts = all_reduce_counts(local_counts, dist, collective_device)
+        self.owner = plan_owners(self.counts, world, cap_units)
+        self.store = Store(desc, self.owner, rank, device, verify)
+        handles = ([self.store.handle()] if dist is None else
+                   all_gather_handles(self.store.handle(), dist, world, collective_device))
+        self.mapped = []
+        bases = []
+        for r in range(world):
+            if r == rank:
+                bases.append(self.store.base)
+            else:
+                b = map_store(handles[r], device)
+                self.mapped.append(b)
+                bases.append(b)
+        self.tier = Tier(world, rank, self.owner, bases, copy)
+        if dist is not None:
+            dist.barrier()
+
+    def close(self):
+        for b in getattr(self, "mapped", []):
+            unmap_store(b)
+        self.mapped = []
+        if getattr(self, "store", None):
+            self.store.close()
+            self.store = None

@@ -68,13 +68,19 @@ class Plan:
 
 
 class DgContext:
-    """A device-gated context (ss_open with forward_mode = SS_FORWARD_DEVICE_GATED)."""
+    """A device-gated context (ss_open with forward_mode = SS_FORWARD_DEVICE_GATED; tsb_open_peer with a peer.Tier,
+    whose stores stay allocated and mapped until close())."""
 
-    def __init__(self, desc, plan, options):
+    def __init__(self, desc, plan, options, peer=None):
         lib = abi.load()
-        self.desc, self.plan = desc, plan
+        self.desc, self.plan, self.peer = desc, plan, peer
         self.h = C.c_void_p()
-        abi.check(lib.ss_open(desc.h, C.byref(plan.budget), plan.h, C.byref(options), C.byref(self.h)))
+        if peer is None:
+            abi.check(lib.ss_open(desc.h, C.byref(plan.budget), plan.h, C.byref(options), C.byref(self.h)))
+        else:
+            t = peer.struct()
+            abi.check(lib.tsb_open_peer(desc.h, C.byref(plan.budget), plan.h, C.byref(options), C.byref(t),
+                                        C.byref(self.h)))
 
     def close(self):
         if getattr(self, "h", None):
