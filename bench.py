@@ -280,7 +280,8 @@ def main():
                                          "writebacks_done", "collected_mid", "wb_forced", "wb_forced_wait_ns",
                                          "wb_boundary_flushed", "wb_deferred", "wb_cancelled", "resurrected",
                                          "wb_issued_bytes", "covered")}
-        peer_stats = json.loads(run.ctx.stats_json())["peer"]
+        full = json.loads(run.ctx.stats_json())
+        peer_stats, open_stats = full["peer"], full["open"]
     finally:
         run.close()
         if setup:  # every rank's context is closed before any store is unmapped or freed
@@ -322,7 +323,7 @@ def main():
                                     "(MEASURED_PEAKS.json has no host-link figure)",
                      "algorithmic_bytes": moved, "device_ms": round(dma_ms, 3)},
         "gpu_launches": int(a.steps * (2 + 2 * LAYERS) + land_launches + a.steps * LAYERS),
-        "clocks": clk, "open_s": round(t_open, 2), "dg": dg,
+        "clocks": clk, "open_s": round(t_open, 2), "open": open_stats, "dg": dg,
         "options": {"wb_defer": a.wb_defer, "wb_stream": a.wb_stream, "spare_slots_per_layer": a.spare,
                     "inclusive_blocks": inclusive},
     }

@@ -50,7 +50,7 @@ def ref():
         lib.oref_host_replay.restype = C.c_int
         lib.oref_host_replay.argtypes = [C.c_char_p, C.c_size_t, C.c_void_p, C.c_size_t, C.c_void_p, C.c_void_p,
                                          C.c_uint32, C.c_void_p, C.c_uint32, C.c_void_p, C.c_void_p, C.c_void_p,
-                                         C.c_char_p, C.c_size_t]
+                                         C.c_void_p, C.c_char_p, C.c_size_t]
         lib.oref_dg_replay.restype = C.c_int
         lib.oref_dg_replay.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
                                        C.c_void_p, C.c_char_p, C.c_size_t]
@@ -58,9 +58,10 @@ def ref():
     return _ref
 
 
-def ref_host_replay(desc_json, tiers, budget, options, routes, all_layers):
+def ref_host_replay(desc_json, tiers, budget, options, routes, all_layers, want_exclusive=False):
     """The reference's host forward mode (CPU backend) over routes [forwards][layers][n_ids]: (locs [forwards][units][2],
-    stats [forwards][layers][5] = routed, hits, admitted, transient, evicted)."""
+    stats [forwards][layers][5] = routed, hits, admitted, transient, evicted[, exclusive [forwards][8] = writebacks,
+    writeback_bytes, deferred, promoted, free_blocks, min_free_blocks, rereads, discards after each forward])."""
     import numpy as np
     routes = np.ascontiguousarray(routes, dtype=np.int32)
     F, L, n = routes.shape
@@ -71,11 +72,13 @@ def ref_host_replay(desc_json, tiers, budget, options, routes, all_layers):
     stats = np.empty((F, L, 5), dtype=np.uint64)
     err = C.create_string_buffer(512)
     raw = desc_json.encode()
+    xs = np.zeros((F, 8), dtype=np.uint64) if want_exclusive else None
     rc = ref().oref_host_replay(raw, len(raw), t.ctypes.data, t.size, C.byref(budget), C.byref(options), F,
-                                routes.ctypes.data, n, al.ctypes.data, locs.ctypes.data, stats.ctypes.data, err, 512)
+                                routes.ctypes.data, n, al.ctypes.data, locs.ctypes.data, stats.ctypes.data,
+                                xs.ctypes.data if xs is not None else None, err, 512)
     if rc != 0:
         raise RuntimeError("reference host replay failed: " + err.value.decode())
-    return locs, stats
+    return (locs, stats, xs) if want_exclusive else (locs, stats)
 
 
 def ref_replay(cfg, ids, preds=None, src_units=None, want_reads=False):

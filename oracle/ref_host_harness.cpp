@@ -37,7 +37,7 @@ struct ss_ctx {
 extern "C" __attribute__((visibility("default"))) int oref_host_replay(
     const char* desc_json, size_t len, const uint8_t* tiers, size_t n_tiers, const ss_budget* budget,
     const ss_options* opt_in, uint32_t forwards, const int32_t* routes, uint32_t n_ids, const uint8_t* all_layers,
-    int32_t* locs, uint64_t* stats, char* err, size_t errlen) {
+    int32_t* locs, uint64_t* stats, uint64_t* xstats, char* err, size_t errlen) {
   ss_desc* d = nullptr;
   ss_plan* p = nullptr;
   ss_ctx* c = nullptr;
@@ -90,6 +90,19 @@ extern "C" __attribute__((visibility("default"))) int oref_host_replay(
       o5[2] = after[size_t(L)].admitted - before[size_t(L)].admitted;
       o5[3] = after[size_t(L)].transient - before[size_t(L)].transient;
       o5[4] = after[size_t(L)].evicted - before[size_t(L)].evicted;
+    }
+    if (xstats) {  // the exclusive counters after the forward (cumulative): writebacks .. discards
+      ss_exclusive_stats x;
+      if (ss_stats_exclusive_sized(c, &x, sizeof x) != SS_OK) return bad("ss_stats_exclusive");
+      uint64_t* o8 = xstats + size_t(f) * 8;
+      o8[0] = x.writebacks;
+      o8[1] = x.writeback_bytes;
+      o8[2] = x.deferred;
+      o8[3] = x.promoted;
+      o8[4] = x.free_blocks;
+      o8[5] = x.min_free_blocks;
+      o8[6] = x.rereads;
+      o8[7] = x.discards;
     }
   }
   ss_close(c);

@@ -148,3 +148,64 @@ def test_layer_all_streams_blobs_through_a_two_slot_ring(orc, ref):
             ctx.end()
     finally:
         ctx.close()
+
+
+@pytest.mark.parametrize("dynamic,spare_units,discard,zipf",
+                         [(2, 4, 0, None), (0, 1, 0, None), (0, 1, 1, None), (0, 2, 0, 1.2), (1, 1, 1, 0.8)])
+def test_c1_exclusive_mode_matches_reference(c1_model, orc, ref, dynamic, spare_units, discard, zipf):
+    """The exclusive tier mode on C1's shape: admissions capped by the free blocks (deferred misses stay transient),
+    victims written back into free blocks before their slots are refilled, promotions freeing their blocks at
+    ss_end, and with exclusive_discard the victims past the free blocks discarded to their files. Per forward and
+    layer the table slots and counters equal the reference's, the eight exclusive counters after every forward equal
+    the reference's, and every unit read through the table has its source bytes."""
+    m = c1_model
+    tiers, b, o = setup(m, dynamic=dynamic, pin_planned=0)
+    b.tier_mode = abi.SS_TIER_MODE_EXCLUSIVE
+    b.host_spare_units = spare_units
+    o.exclusive_discard = discard
+    if zipf:
+        routes = synth.zipf_trace(48, m.layers, m.units, 2, s=zipf, seed=3)
+    else:
+        routes = synth.zipf_trace(48, m.layers, m.units, 2, seed=1, uniform=True)
+    desc_json = m.desc(order="ranked", tiers="pinned|disk" if discard else "pinned")
+    ref_locs, ref_stats, ref_x = oracle.ref_host_replay(desc_json, tiers, b, o, routes, [0] * m.layers,
+                                                        want_exclusive=True)
+    assert ref_x[-1][0] > 0, "the trace must write back"
+    if dynamic == 0 and not discard:
+        assert ref_x[-1][2] > 0, "few free blocks must defer admissions"
+    if discard:
+        assert ref_x[-1][7] > 0, "victims past the free blocks must be discarded"
+    desc = runtime.Desc(desc_json)
+    plan = runtime.Plan(desc, b, tiers=tiers)
+    ctx = runtime.HostContext(desc, plan, o)
+    eng = abi.load_engine()
+    want = expected(m, orc)
+    s = torch.cuda.Stream()
+    ids_dev = torch.zeros(m.units, dtype=torch.int32, device="cuda")
+    out = torch.zeros(m.units, dtype=torch.int64, device="cuda")
+    try:
+        for f in range(routes.shape[0]):
+            before = [ctx.layer_stats(L) for L in range(m.layers)]
+            ctx.begin()
+            for L in range(m.layers):
+                ctx.routes(L, routes[f, L])
+                v = ctx.acquire(L, s.cuda_stream)
+                assert np.array_equal(ctx.locs(L, m.units), ref_locs[f, L * m.units:(L + 1) * m.units]), \
+                    "forward %d layer %d: table differs from the reference" % (f, L)
+                ids = np.unique(routes[f, L]).astype(np.int32)
+                with torch.cuda.stream(s):
+                    ids_dev[:ids.size].copy_(torch.from_numpy(ids), non_blocking=False)
+                    assert eng.tse_read_table(C_ptr(v.table_dev), ids_dev.data_ptr(), ids.size, m.unit_bytes,
+                                              out.data_ptr(), 16, s.cuda_stream) == 0
+                s.synchronize()
+                got = out[:ids.size].cpu().numpy().astype(np.uint64)
+                assert np.array_equal(got, want[L * m.units + ids]), "forward %d layer %d: wrong bytes" % (f, L)
+                ctx.release(L, s.cuda_stream)
+            ctx.end()
+            for L in range(m.layers):
+                a = ctx.layer_stats(L)
+                mine = [a[k] - before[L][k] for k in ("routed", "hits", "admitted", "transient", "evicted")]
+                assert mine == [int(x) for x in ref_stats[f, L]], "forward %d layer %d counters" % (f, L)
+            assert ctx.exclusive_stats() == [int(x) for x in ref_x[f]], "forward %d exclusive counters" % f
+    finally:
+        ctx.close()

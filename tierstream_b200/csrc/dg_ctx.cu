@@ -1061,14 +1061,15 @@ class CudaDgContext final : public DgContext {
   std::string stats_json() const override {
     ss_dg_stats s;
     stats(&s);
-    char buf[1024];
+    char buf[2048];
     std::snprintf(buf, sizeof buf,
                   "{\"schema\":\"strix-stream/stats-v1\",\"mode\":\"device-gated\",\"copy\":\"%s\","
                   "\"dg\":{\"tokens\":%llu,\"lookups\":%llu,\"misses\":%llu,\"covered\":%llu,\"fetched\":%llu,"
                   "\"prefetched\":%llu,\"bank_serves\":%llu,\"evicted\":%llu,\"resurrected\":%llu,"
                   "\"writebacks_done\":%llu,\"wb_issued_bytes\":%llu,\"free_slots\":%llu,\"land_launches\":%llu,"
                   "\"dma_ms_total\":%.6f,\"open_seconds\":%.3f},\"peer\":{\"world\":%u,\"rank\":%d,"
-                  "\"all_owned\":%d,\"copy\":\"%s\",\"peer_units\":%llu,\"self_units\":%llu}}",
+                  "\"all_owned\":%d,\"copy\":\"%s\",\"peer_units\":%llu,\"self_units\":%llu},"
+                  "\"open\":{\"alloc_s\":%.3f,\"fill_pinned_s\":%.3f,\"fill_residents_s\":%.3f,\"verify_s\":%.3f}}",
                   mover_->kernel_copies() ? "land-kernel" : "copy-engine", (unsigned long long)s.tokens,
                   (unsigned long long)s.lookups, (unsigned long long)s.misses, (unsigned long long)s.covered,
                   (unsigned long long)s.fetched, (unsigned long long)s.prefetched, (unsigned long long)s.bank_serves,
@@ -1077,7 +1078,8 @@ class CudaDgContext final : public DgContext {
                   (unsigned long long)s.free_slots, (unsigned long long)mover_->kernel_launches(),
                   mover_->dma_total_ms(), open_seconds_, peer_ ? peer_->world : 0u, peer_ ? peer_->rank : -1,
                   peer_ && peer_->all_owned ? 1 : 0, peer_ && peer_->copy == 1 ? "copy-engine" : "land-kernel",
-                  (unsigned long long)mover_->peer_units(), (unsigned long long)mover_->self_units());
+                  (unsigned long long)mover_->peer_units(), (unsigned long long)mover_->self_units(), open_alloc_s_,
+                  open_fill_pinned_s_, open_fill_res_s_, open_verify_s_);
     return buf;
   }
   void reset_open() override {
@@ -1321,6 +1323,7 @@ class CudaDgContext final : public DgContext {
     order.insert(order.end(), x_.residents.begin(), x_.residents.end());
     for (uint32_t k = 0; k < x_.keys; ++k) order.push_back(k);
     core_->place(order);
+    open_alloc_s_ = std::chrono::duration<double>(Clock::now() - t_start).count();
     fill();
     mover_->upload_table(core_->table().data(), x_.keys);
     core_->check();
@@ -1337,6 +1340,7 @@ class CudaDgContext final : public DgContext {
   // lands through a pinned staging ring; with verify_hash and descriptor hashes, pinned units are hashed on the host
   // and residents on the device (one K3 launch over every resident slot) before the first token.
   void fill() {
+    const auto t_fill = Clock::now();
     const uint32_t G = uint32_t(x_.gated.size());
     std::vector<std::pair<uint32_t, uint32_t>> res, pin, from_store;  // (g, unit)
     for (uint32_t g = 0; g < G; ++g)
@@ -1386,6 +1390,7 @@ class CudaDgContext final : public DgContext {
                           ") differs from its descriptor hash");
         },
         pin.size());
+    const auto t_pinned = Clock::now();
     // residents: through a ring of pinned staging units, nthreads at a time
     const size_t ring = std::min<size_t>(std::max<size_t>(res.size(), 1), nthreads);
     std::vector<char*> stage(ring, nullptr);
@@ -1421,7 +1426,11 @@ class CudaDgContext final : public DgContext {
     }
     ck(cudaStreamSynchronize(fs), "cudaStreamSynchronize (fill from store)");
     res.insert(res.end(), from_store.begin(), from_store.end());
+    const auto t_res = Clock::now();
     if (verify && !res.empty() && hash_of(0, 0)) verify_residents(res);
+    open_fill_pinned_s_ = std::chrono::duration<double>(t_pinned - t_fill).count();
+    open_fill_res_s_ = std::chrono::duration<double>(t_res - t_pinned).count();
+    open_verify_s_ = std::chrono::duration<double>(Clock::now() - t_res).count();
   }
 
   // K3 over every resident slot at once: the arena's bytes against the descriptor's hashes.
@@ -1513,7 +1522,7 @@ class CudaDgContext final : public DgContext {
   uint64_t evicted_before_ = 0;
   ss_dg_boundary_timeline boundary_{};
   std::vector<double> gpu_wait_us_, gpu_ready_us_;
-  double open_seconds_ = 0;
+  double open_seconds_ = 0, open_alloc_s_ = 0, open_fill_pinned_s_ = 0, open_fill_res_s_ = 0, open_verify_s_ = 0;
 };
 
 }  // namespace

@@ -10,6 +10,13 @@
 //
 // Copies from the pinned tier go through the copy engines for units of at least 8 MiB (they measured faster there on
 // B200) and through the land kernel (kernels.cu, one launch for every unit of a routes call) below that.
+//
+// Exclusive tier mode (budget tier_mode EXCLUSIVE; stream_ctx.cpp:1030-1126, 1640-1665 there): a unit lives in a slot
+// or in a pinned block, never both. An admission evicts at most as many victims as the layer's block class has free
+// blocks (the rest of its misses stay transient and count as deferred), writes each victim back into a free block on
+// the write-back stream before the admitted unit's copy into that slot starts, and a unit promoted from its block
+// frees the block at ss_end. With exclusive_discard the evictions are uncapped and victims past the free blocks are
+// discarded to their files.
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -52,6 +59,8 @@ struct Job {
   char* dst = nullptr;             // device slot
   const char* pinned = nullptr;    // pinned tier source, null = its file
   cudaEvent_t wait_ev = nullptr;   // the copy waits for it (the slot's last readers)
+  cudaEvent_t src_wait_ev = nullptr;  // exclusive: the write-back into its block that has to land first
+  cudaEvent_t dst_wb_ev = nullptr;    // exclusive: the write-back of the victim whose slot it lands in
   cudaEvent_t done_ev = nullptr;   // recorded on the copy stream after the copy
   std::atomic<int> state{Queued};
   ss_status err_status = SS_OK;
@@ -109,6 +118,10 @@ class HostCtx final : public HostContext {
     }
     ck(cudaStreamSynchronize(copy_), "cudaStreamSynchronize (seed)");
     for (const JobPtr& j : jobs) pool_ev(j->done_ev);
+    // exclusive: a seeded unit's copy out of its block has completed (stream sync): the block is free at once
+    if (excl_)
+      for (const JobPtr& j : jobs)
+        if (j->state.load() == Job::Done) free_block(layer, j->unit);
     if (st != SS_OK) fail(st, err);
   }
 
@@ -130,6 +143,10 @@ class HostCtx final : public HostContext {
       s.skip = rows ? rows[L] == 0 : false;
     }
     std::fill(fwd_.begin(), fwd_.end(), ss_layer_stats{});
+    if (excl_) {
+      xst_.free_blocks = free_block_count();
+      xst_.min_free_blocks = std::min(xst_.min_free_blocks, xst_.free_blocks);
+    }
     stream_set_ = false;
     in_fwd_ = true;
   }
@@ -290,6 +307,33 @@ class HostCtx final : public HostContext {
         s.ready_wait = true;
       }
     }
+    // exclusive: promotions free their blocks; the copy stream waits for this forward's write-backs (every block
+    // they wrote is complete before a later forward reads it), then marks blocks_ev_ after every copy of this forward
+    // (the next forward's first write-back waits for it before reusing a freed block or reading a slot filled now)
+    if (excl_) {
+      for (size_t L = 0; L < L_.size(); ++L) {
+        Lay& s = L_[L];
+        if (!s.rs) continue;
+        for (int u = 0; u < d_.layers[L].n_units; ++u)
+          if (s.loc[size_t(u)] == kPersistent && s.job[size_t(u)] && s.job[size_t(u)]->pinned &&
+              s.job[size_t(u)]->state.load() == Job::Done)
+            free_block(int(L), u);
+      }
+      {
+        std::lock_guard<std::mutex> lk(copy_mu_);
+        if (!wb_evs_.empty()) {
+          ck(cudaEventRecord(wb_mark_ev_, wb_stream_), "cudaEventRecord (write-back mark)");
+          ck(cudaStreamWaitEvent(copy_, wb_mark_ev_, 0), "cudaStreamWaitEvent (write-back mark)");
+        }
+        ck(cudaEventRecord(blocks_ev_, copy_), "cudaEventRecord (blocks)");
+        wb_gate_ = true;
+      }
+      for (int64_t g : wb_units_) wb_pending_[size_t(g)] = nullptr;
+      wb_units_.clear();
+      for (cudaEvent_t e : wb_evs_) pool_ev(e);
+      wb_evs_.clear();
+      xst_.free_blocks = free_block_count();
+    }
     for (const JobPtr& j : fwd_jobs_) pool_ev(j->done_ev);
     fwd_jobs_.clear();
     ss_layer_stats tot{};
@@ -342,21 +386,27 @@ class HostCtx final : public HostContext {
     hook_user_ = user;
   }
   void exclusive_stats(ss_exclusive_stats* out) const override {
-    *out = ss_exclusive_stats{};
+    *out = xst_;
     out->struct_size = uint32_t(sizeof *out);
   }
   std::string stats_json() const override {
     ss_layer_stats t;
     total_stats(&t);
-    char buf[512];
+    char buf[1024];
     std::snprintf(buf, sizeof buf,
                   "{\"schema\":\"strix-stream/stats-v1\",\"mode\":\"host\",\"forwards\":%llu,\"total\":{\"routed\":%llu,"
                   "\"hits\":%llu,\"admitted\":%llu,\"transient\":%llu,\"evicted\":%llu,\"bytes_pinned\":%llu,"
-                  "\"bytes_disk\":%llu,\"wait_ns\":%llu},\"land_launches\":%llu}",
+                  "\"bytes_disk\":%llu,\"wait_ns\":%llu},\"land_launches\":%llu,\"exclusive\":{\"on\":%d,"
+                  "\"writebacks\":%llu,\"writeback_bytes\":%llu,\"deferred\":%llu,\"promoted\":%llu,"
+                  "\"free_blocks\":%llu,\"min_free_blocks\":%llu,\"rereads\":%llu,\"discards\":%llu}}",
                   (unsigned long long)forwards_, (unsigned long long)t.routed, (unsigned long long)t.hits,
                   (unsigned long long)t.admitted, (unsigned long long)t.transient, (unsigned long long)t.evicted,
                   (unsigned long long)t.bytes_pinned, (unsigned long long)t.bytes_disk, (unsigned long long)t.wait_ns,
-                  (unsigned long long)land_launches_);
+                  (unsigned long long)land_launches_, excl_ ? 1 : 0, (unsigned long long)xst_.writebacks,
+                  (unsigned long long)xst_.writeback_bytes, (unsigned long long)xst_.deferred,
+                  (unsigned long long)xst_.promoted, (unsigned long long)xst_.free_blocks,
+                  (unsigned long long)xst_.min_free_blocks, (unsigned long long)xst_.rereads,
+                  (unsigned long long)xst_.discards);
     return buf;
   }
 
@@ -461,6 +511,10 @@ class HostCtx final : public HostContext {
     j->dst = dst;
     j->wait_ev = L_[size_t(layer)].release_ev;
     j->pinned = pinned_of_[size_t(gidx(layer, unit))];
+    if (excl_ && j->pinned) {
+      j->src_wait_ev = wb_pending_[size_t(gidx(layer, unit))];
+      if (j->src_wait_ev) ++xst_.rereads;
+    }
     j->done_ev = event();
     return j;
   }
@@ -480,8 +534,11 @@ class HostCtx final : public HostContext {
   void flush_copies() {
     if (batch_.empty()) return;
     std::lock_guard<std::mutex> lk(copy_mu_);
-    for (const JobPtr& j : batch_)
+    for (const JobPtr& j : batch_) {
       if (j->wait_ev) ck(cudaStreamWaitEvent(copy_, j->wait_ev, 0), "cudaStreamWaitEvent (slot reuse)");
+      if (j->src_wait_ev) ck(cudaStreamWaitEvent(copy_, j->src_wait_ev, 0), "cudaStreamWaitEvent (block written)");
+      if (j->dst_wb_ev) ck(cudaStreamWaitEvent(copy_, j->dst_wb_ev, 0), "cudaStreamWaitEvent (victim written back)");
+    }
     // the land kernel for small units (one launch for the batch), the copy engines for large ones
     auto kb = std::make_unique<dev::Batch>();
     auto launch = [&] {
@@ -551,6 +608,8 @@ class HostCtx final : public HostContext {
         {
           std::lock_guard<std::mutex> lk(copy_mu_);
           if (j->wait_ev) ck(cudaStreamWaitEvent(copy_, j->wait_ev, 0), "cudaStreamWaitEvent (slot reuse)");
+          if (j->dst_wb_ev)
+            ck(cudaStreamWaitEvent(copy_, j->dst_wb_ev, 0), "cudaStreamWaitEvent (victim written back)");
           ck(cudaMemcpyAsync(j->dst, s, size_t(l.unit_bytes), cudaMemcpyHostToDevice, copy_), "cudaMemcpyAsync (read)");
           ck(cudaEventRecord(j->done_ev, copy_), "cudaEventRecord (read)");
         }
@@ -612,9 +671,10 @@ class HostCtx final : public HostContext {
     }
     return false;
   }
-  void fetch_into_persistent(int layer, int unit, int slot) {
+  void fetch_into_persistent(int layer, int unit, int slot, cudaEvent_t dst_wb_ev = nullptr) {
     Lay& s = L_[size_t(layer)];
     JobPtr j = make_job(layer, unit, at(s.pool, uint64_t(slot) * stride(layer)));
+    j->dst_wb_ev = dst_wb_ev;
     fwd_jobs_.push_back(j);
     s.loc[size_t(unit)] = kPersistent;
     s.slot[size_t(unit)] = slot;
@@ -623,6 +683,91 @@ class HostCtx final : public HostContext {
         d_.layers[size_t(layer)].unit_bytes;
     submit(j);
   }
+  // ---- exclusive tier mode ----
+  int block_class(int layer) const { return excl_ ? layer_class_[size_t(layer)] : -1; }
+  uint64_t free_block_count() const {
+    uint64_t f = 0;
+    for (const auto& v : free_blocks_) f += v.size();
+    return f;
+  }
+  // Evictions an admission may make: one free block per victim; uncapped with exclusive_discard.
+  int eviction_cap(int layer) const {
+    if (!excl_) return -1;
+    const int cls = block_class(layer);
+    if (cls < 0) return 0;
+    if (o_.exclusive_discard) return -1;
+    return int(std::min<uint64_t>(free_blocks_[size_t(cls)].size(), uint64_t(INT32_MAX)));
+  }
+  // The admission's victims into free blocks on the write-back stream (the first ones, in ascending unit order, while
+  // blocks last; with exclusive_discard the rest are discarded to their files). Returns the event the admitted units'
+  // copies into those slots wait for, null when nothing is written back.
+  cudaEvent_t write_back(int layer, const Admission& a, size_t* n_wb) {
+    const Layer& l = d_.layers[size_t(layer)];
+    const Lay& s = L_[size_t(layer)];
+    const int cls = block_class(layer);
+    const uint64_t room = cls < 0 ? 0 : free_blocks_[size_t(cls)].size();
+    if (cls < 0 || (!o_.exclusive_discard && room < a.evicted.size()))
+      fail(SS_E_BACKEND, "exclusive: more victims than free blocks (internal)");
+    const size_t nw = size_t(std::min<uint64_t>(room, a.evicted.size()));
+    *n_wb = nw;
+    for (int32_t u : a.evicted)
+      if (pinned_of_[size_t(gidx(layer, u))])
+        fail(SS_E_BACKEND, "exclusive: an evicted resident still owns a block (internal)");
+    xst_.discards += a.evicted.size() - nw;  // a discard copies nothing and takes no block
+    if (!nw) return nullptr;
+    std::lock_guard<std::mutex> lk(copy_mu_);
+    if (wb_gate_) {  // the copies of earlier forwards (into these slots, out of these blocks) come first
+      ck(cudaStreamWaitEvent(wb_stream_, blocks_ev_, 0), "cudaStreamWaitEvent (blocks)");
+      wb_gate_ = false;
+    }
+    cudaEvent_t ev = event();
+    wb_evs_.push_back(ev);
+    auto kb = std::make_unique<dev::Batch>();
+    for (size_t i = 0; i < nw; ++i) {
+      const int64_t g = gidx(layer, a.evicted[i]);
+      char* b = free_blocks_[size_t(cls)].back();
+      free_blocks_[size_t(cls)].pop_back();
+      pinned_of_[size_t(g)] = b;
+      const char* src = at(s.pool, uint64_t(a.evicted_slot[i]) * stride(layer));
+      if (l.unit_bytes >= ce_min_) {
+        ck(cudaMemcpyAsync(b, src, size_t(l.unit_bytes), cudaMemcpyDeviceToHost, wb_stream_),
+           "cudaMemcpyAsync (write-back)");
+      } else {
+        if (kb->n_copies == dev::kMaxCopies) launch_batch_on(*kb, wb_stream_);
+        kb->copies[kb->n_copies++] = {src, b, l.unit_bytes};
+      }
+      ++xst_.writebacks;
+      xst_.writeback_bytes += l.unit_bytes;
+    }
+    launch_batch_on(*kb, wb_stream_);
+    ck(cudaEventRecord(ev, wb_stream_), "cudaEventRecord (write-back)");
+    for (size_t i = 0; i < nw; ++i) {  // published after the record: a read of one of these blocks waits for it
+      const int64_t g = gidx(layer, a.evicted[i]);
+      wb_pending_[size_t(g)] = ev;
+      wb_units_.push_back(g);
+    }
+    return ev;
+  }
+  // A unit that landed in a slot from its block no longer owns the block (its copy was issued; the block's next
+  // writer waits for that copy through blocks_ev_ or a stream sync).
+  void free_block(int layer, int unit) {
+    const int64_t g = gidx(layer, unit);
+    char* b = const_cast<char*>(pinned_of_[size_t(g)]);
+    if (!b) return;
+    free_blocks_[size_t(block_class(layer))].push_back(b);
+    pinned_of_[size_t(g)] = nullptr;
+    ++xst_.promoted;
+  }
+  void launch_batch_on(dev::Batch& kb, cudaStream_t st) {
+    if (!kb.n_copies) return;
+    uint64_t chunks = 0;
+    for (uint32_t i = 0; i < kb.n_copies; ++i) chunks += (kb.copies[i].bytes + (64u << 10) - 1) >> 16;
+    ck(cudaError_t(dev::launch_batch(kb, int(std::min<uint64_t>(std::max<uint64_t>(chunks, 1), 296)), st)),
+       "land kernel");
+    ++land_launches_;
+    kb.n_copies = 0;
+  }
+
   void dispatch_pending() {
     for (size_t L = 0; L < L_.size(); ++L) {
       Lay& s = L_[L];
@@ -659,8 +804,17 @@ class HostCtx final : public HostContext {
     }
     st.routed += s.routed.size();
     st.hits += s.hits.size();
-    const Admission a = s.rs->admit(to_admit, busy, true, -1);
-    for (size_t k = 0; k < a.admitted.size(); ++k) fetch_into_persistent(layer, a.admitted[k], a.slot_of[k]);
+    const Admission a = s.rs->admit(to_admit, busy, true, eviction_cap(layer));
+    xst_.deferred += uint64_t(a.deferred);
+    // exclusive: the victims go back to free blocks first; only a copy into a written-back victim's slot waits
+    size_t n_wb = 0;
+    cudaEvent_t wb_ev = excl_ && !a.evicted.empty() ? write_back(layer, a, &n_wb) : nullptr;
+    for (size_t k = 0; k < a.admitted.size(); ++k) {
+      cudaEvent_t wait = nullptr;
+      for (size_t i = 0; wb_ev && i < n_wb && !wait; ++i)
+        if (a.evicted_slot[i] == a.slot_of[k]) wait = wb_ev;
+      fetch_into_persistent(layer, a.admitted[k], a.slot_of[k], wait);
+    }
     for (int32_t u : a.transient)
       if (!fetch_into_ring(layer, u)) {
         s.pending.push_back(u);
@@ -675,9 +829,11 @@ class HostCtx final : public HostContext {
 
   void init() {
     require(int64_t(plan_.tier.size()) == d_.total_units, SS_E_INVALID, "open: plan does not match the descriptor");
-    require(b_.tier_mode == SS_TIER_MODE_INCLUSIVE, SS_E_UNSUPPORTED,
-            "open: the exclusive tier mode of the host forward mode is not in this build (the device-gated mode is "
-            "exclusive)");
+    excl_ = b_.tier_mode == SS_TIER_MODE_EXCLUSIVE;
+    // a resident's slot is the only copy an eviction writes back: it must hold the unit's bytes from open
+    require(!(excl_ && !o_.fill_residents), SS_E_INVALID, "open: the exclusive tier mode needs fill_residents = 1");
+    require(!(excl_ && o_.exclusive_discard && d_.tiers == Tiers::Pinned), SS_E_INVALID,
+            "open: exclusive_discard needs a descriptor whose tiers allow disk (tiers = \"pinned\" refuses it)");
     require(o_.readahead_units == 0, SS_E_UNSUPPORTED, "open: host read-ahead is not in this build");
     ck(cudaSetDevice(o_.device), "cudaSetDevice");
     ck_launch_preload();
@@ -702,6 +858,47 @@ class HostCtx final : public HostContext {
     }
     for (int64_t g = 0; g < d_.total_units; ++g)
       if (pl.chunk_of[size_t(g)] >= 0) pinned_of_[size_t(g)] = at(chunks_[size_t(pl.chunk_of[size_t(g)])], pl.offset_of[size_t(g)]);
+    // exclusive: one block class per host stride, the plan's spare blocks (<= 1 GiB chunks, mapped: the land kernel
+    // writes victims into them), the write-back stream and its events
+    if (excl_) {
+      ck(cudaStreamCreateWithFlags(&wb_stream_, cudaStreamNonBlocking), "cudaStreamCreate (write-back)");
+      ck(cudaEventCreateWithFlags(&blocks_ev_, cudaEventDisableTiming), "cudaEventCreate");
+      ck(cudaEventCreateWithFlags(&wb_mark_ev_, cudaEventDisableTiming), "cudaEventCreate");
+      wb_pending_.assign(size_t(d_.total_units), nullptr);
+      std::vector<uint64_t> block_bytes;
+      for (const tsb::SpareClass& c : plan_.spares) block_bytes.push_back(c.block_bytes);
+      free_blocks_.resize(block_bytes.size());
+      layer_class_.assign(d_.layers.size(), -1);
+      std::vector<uint64_t> class_total(block_bytes.size(), 0);
+      for (size_t L = 0; L < d_.layers.size(); ++L) {
+        const Layer& l = d_.layers[L];
+        if (!l.streamable || !l.n_units) continue;
+        const auto it = std::find(block_bytes.begin(), block_bytes.end(), host_stride(l.unit_bytes));
+        require(it != block_bytes.end(), SS_E_INVALID, "open: exclusive plan without a block class (internal)");
+        layer_class_[L] = int(it - block_bytes.begin());
+        for (int u = 0; u < l.n_units; ++u)
+          if (pinned_of_[size_t(gidx(int(L), u))]) ++class_total[size_t(layer_class_[L])];
+      }
+      for (size_t k = 0; k < plan_.spares.size(); ++k) {
+        const uint64_t bytes = plan_.spares[k].block_bytes;
+        const uint64_t per_chunk = std::max<uint64_t>(1, (uint64_t(1) << 30) / bytes);
+        free_blocks_[k].reserve(size_t(class_total[k] + plan_.spares[k].blocks));  // never reallocates later
+        std::vector<char*> blocks;
+        for (uint64_t left = plan_.spares[k].blocks; left > 0;) {
+          const uint64_t n = std::min(per_chunk, left);
+          void* chunk = nullptr;
+          ck(cudaHostAlloc(&chunk, size_t(n * bytes), cudaHostAllocMapped | cudaHostAllocPortable),
+             "cudaHostAlloc (spare blocks)");
+          spare_chunks_.push_back(chunk);
+          for (uint64_t i = 0; i < n; ++i) blocks.push_back(at(chunk, i * bytes));
+          left -= n;
+        }
+        for (size_t i = blocks.size(); i-- > 0;) free_blocks_[k].push_back(blocks[i]);
+        xst_.free_blocks += plan_.spares[k].blocks;
+      }
+      xst_.min_free_blocks = xst_.free_blocks;
+      wb_units_.reserve(size_t(d_.total_units));
+    }
     // staging for file reads: one unit of the largest file-tier unit each
     uint64_t disk_unit = 0;
     for (size_t L = 0; L < d_.layers.size(); ++L)
@@ -840,6 +1037,7 @@ class HostCtx final : public HostContext {
       if (t.joinable()) t.join();
     workers_.clear();
     if (copy_) cudaStreamSynchronize(copy_);
+    if (wb_stream_) cudaStreamSynchronize(wb_stream_);
     cudaDeviceSynchronize();
     for (Lay& s : L_) {
       if (s.pool) cudaFree(s.pool);
@@ -856,6 +1054,13 @@ class HostCtx final : public HostContext {
     ring_bases_.clear();
     for (void* c : chunks_) cudaFreeHost(c);
     chunks_.clear();
+    for (void* c : spare_chunks_) cudaFreeHost(c);
+    spare_chunks_.clear();
+    if (wb_stream_) cudaStreamDestroy(wb_stream_);
+    wb_stream_ = nullptr;
+    if (blocks_ev_) cudaEventDestroy(blocks_ev_);
+    if (wb_mark_ev_) cudaEventDestroy(wb_mark_ev_);
+    blocks_ev_ = wb_mark_ev_ = nullptr;
     for (char* s : staging_) cudaFreeHost(s);
     staging_.clear();
     for (cudaEvent_t e : all_ev_) cudaEventDestroy(e);
@@ -895,6 +1100,17 @@ class HostCtx final : public HostContext {
   bool in_fwd_ = false, poisoned_ = false, stream_set_ = false;
   void* stream_ = nullptr;
   uint64_t forwards_ = 0, ce_min_ = 0, land_launches_ = 0;
+  // exclusive tier mode
+  bool excl_ = false, wb_gate_ = false;
+  cudaStream_t wb_stream_ = nullptr;
+  cudaEvent_t blocks_ev_ = nullptr, wb_mark_ev_ = nullptr;
+  std::vector<cudaEvent_t> wb_pending_;  // per unit: the write-back into its block this forward
+  std::vector<int64_t> wb_units_;
+  std::vector<cudaEvent_t> wb_evs_;
+  std::vector<int> layer_class_;                 // per layer: its block class (-1: none)
+  std::vector<std::vector<char*>> free_blocks_;  // per class, the lowest address last (taken first)
+  std::vector<void*> spare_chunks_;
+  ss_exclusive_stats xst_{};
 };
 
 }  // namespace

@@ -183,6 +183,12 @@ class HostContext:
     def check_unit(self, layer, unit):
         abi.check(abi.load().ss_check_unit(self.h, layer, unit))
 
+    def exclusive_stats(self):
+        x = abi.ss_exclusive_stats()
+        abi.check(abi.load().ss_stats_exclusive_sized(self.h, C.byref(x), C.sizeof(x)))
+        return [x.writebacks, x.writeback_bytes, x.deferred, x.promoted, x.free_blocks, x.min_free_blocks,
+                x.rereads, x.discards]
+
 
 class TokenGraph:
     """One decode step captured once (libtsb_engine.so): begin, per layer export / wait / reader, end."""
