@@ -1265,21 +1265,50 @@ class CudaDgContext final : public DgContext {
     }
     gpu_wait_us_.assign(G, -1);
     gpu_ready_us_.assign(G, -1);
-    // pinned blocks (mapped: the land kernel reads them), <= 1 GiB chunks; the reset staging unit
+    // pinned blocks (mapped: the land kernel reads them), <= 1 GiB chunks allocated by a pool of threads (pinning the
+    // pages is the open's longest step, and the driver pins chunks of different threads side by side); the reset
+    // staging unit
     const uint64_t hs = x_.host_stride;
     const uint64_t per_chunk = std::max<uint64_t>(1, (uint64_t(1) << 30) / hs);
+    std::vector<uint64_t> chunk_units;
     for (uint64_t left = peer_ && peer_->all_owned ? 0 : x_.blocks; left > 0;) {
-      const uint64_t n = std::min(per_chunk, left);
-      void* p = nullptr;
-      ck(cudaHostAlloc(&p, size_t(n * hs), cudaHostAllocMapped | cudaHostAllocPortable), "cudaHostAlloc (blocks)");
-      chunks_.push_back(p);
+      chunk_units.push_back(std::min(per_chunk, left));
+      left -= chunk_units.back();
+    }
+    chunks_.assign(chunk_units.size(), nullptr);
+    {
+      std::atomic<size_t> next{0};
+      std::mutex err_mu;
+      std::string err;
+      const size_t nth = std::min<size_t>(chunk_units.size(), 8);
+      std::vector<std::thread> th;
+      for (size_t t = 0; t < nth; ++t)
+        th.emplace_back([&] {
+          if (cudaSetDevice(device_) != cudaSuccess) return;
+          for (;;) {
+            const size_t i = next.fetch_add(1);
+            if (i >= chunk_units.size()) return;
+            void* p = nullptr;
+            const cudaError_t e = cudaHostAlloc(&p, size_t(chunk_units[i] * hs), cudaHostAllocMapped | cudaHostAllocPortable);
+            if (e != cudaSuccess) {
+              (void)cudaGetLastError();
+              std::lock_guard<std::mutex> lk(err_mu);
+              if (err.empty()) err = std::string("cudaHostAlloc (blocks): ") + cudaGetErrorString(e);
+              return;
+            }
+            chunks_[i] = p;
+          }
+        });
+      for (auto& t : th) t.join();
+      if (!err.empty()) fail(SS_E_NOMEM, "device-gated: " + err);
+    }
+    for (size_t c = 0; c < chunks_.size(); ++c) {
       void* pd = nullptr;
-      ck(cudaHostGetDevicePointer(&pd, p, 0), "cudaHostGetDevicePointer (blocks)");
-      for (uint64_t i = 0; i < n; ++i) {
-        bufs_.blocks.push_back(static_cast<char*>(p) + i * hs);
+      ck(cudaHostGetDevicePointer(&pd, chunks_[c], 0), "cudaHostGetDevicePointer (blocks)");
+      for (uint64_t i = 0; i < chunk_units[c]; ++i) {
+        bufs_.blocks.push_back(static_cast<char*>(chunks_[c]) + i * hs);
         bufs_.blocks_d.push_back(static_cast<char*>(pd) + i * hs);
       }
-      left -= n;
     }
     ck(cudaHostAlloc(reinterpret_cast<void**>(&bufs_.staging), size_t(hs), cudaHostAllocMapped | cudaHostAllocPortable),
        "cudaHostAlloc (staging)");
@@ -1492,7 +1521,8 @@ class CudaDgContext final : public DgContext {
     if (ctl_) cudaFree(ctl_);
     if (mapped_h_) cudaFreeHost(mapped_h_);
     if (stamps_h_) cudaFreeHost(stamps_h_);
-    for (void* c : chunks_) cudaFreeHost(c);
+    for (void* c : chunks_)
+      if (c) cudaFreeHost(c);
     if (bufs_.staging) cudaFreeHost(bufs_.staging);
   }
 

@@ -281,25 +281,17 @@ __global__ __launch_bounds__(32) void xxh64_kernel(const HashUnit* __restrict__ 
     const uint64_t start = uint64_t(c) * kHashChunk;
     const uint32_t n0 = start < body0 ? uint32_t((body0 - start < kHashChunk ? body0 - start : kHashChunk) / 32) : 0u;
     const uint32_t n1 = start < body1 ? uint32_t((body1 - start < kHashChunk ? body1 - start : kHashChunk) / 32) : 0u;
-    // batches of 8 stripes: the loads and the w * X2 products (off the chains) first, then the two chains' steps
-    // interleaved, so each step waits only on its own chain
-    const uint32_t both = n0 < n1 ? n0 : n1;
-    uint32_t s = 0;
-    for (; s + 8 <= both; s += 8) {
-      uint64_t p0[8], p1[8];
-#pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        p0[k] = w0[4 * (s + k)] * X2;
-        p1[k] = w1[4 * (s + k)] * X2;
+    // the two chains' steps interleaved: each step waits only on its own chain
+    if (n0 == kHashChunk / 32 && n1 == kHashChunk / 32) {
+#pragma unroll 16
+      for (int s = 0; s < kHashChunk / 32; ++s) {
+        a0 = lane_step(a0, w0[4 * s]);
+        a1 = lane_step(a1, w1[4 * s]);
       }
-#pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        a0 = rotl64(a0 + p0[k], 31) * X1;
-        a1 = rotl64(a1 + p1[k], 31) * X1;
-      }
+    } else {
+      for (uint32_t s = 0; s < n0; ++s) a0 = lane_step(a0, w0[4 * s]);
+      for (uint32_t s = 0; s < n1; ++s) a1 = lane_step(a1, w1[4 * s]);
     }
-    for (uint32_t t = s; t < n0; ++t) a0 = lane_step(a0, w0[4 * t]);
-    for (uint32_t t = s; t < n1; ++t) a1 = lane_step(a1, w1[4 * t]);
     __syncwarp();  // every lane is done with the stage before it is refilled
     if (c + kHashStages < nchunks) issue(c + kHashStages);
   }
