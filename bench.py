@@ -203,7 +203,7 @@ def main():
     if world > 1:
         import datetime
         import torch.distributed as dist
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600))
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device("cuda", local))
 
     def barrier():
         if dist:

@@ -136,3 +136,28 @@ def test_stopped_service_times_out_on_the_device(small_model):
         assert e.value.status == abi.SS_E_BACKEND
     finally:
         run.close()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_context_on_another_device_keeps_the_callers_device(small_model):
+    """A context opened (and driven, and closed) for device 1 from a thread whose current device is 0 runs there and
+    leaves the thread on device 0 after every call."""
+    m = small_model
+    torch.cuda.set_device(1)
+    run = harness.DgRun(m, residents_per_layer=3, max_ids=2)
+    try:
+        assert torch.cuda.current_device() == 1  # the open switched to device 1 and back
+        torch.cuda.set_device(0)
+        run.ctx.check()  # the library switches to device 1 inside the call and back
+        assert torch.cuda.current_device() == 0
+        torch.cuda.set_device(1)
+        ids = synth.zipf_trace(3, m.layers, m.units, 2, s=1.0, seed=2)
+        for t in range(3):
+            run.step(ids[t])
+        torch.cuda.set_device(0)
+        run.ctx.check()
+        assert torch.cuda.current_device() == 0
+    finally:
+        torch.cuda.set_device(1)
+        run.close()
+        torch.cuda.set_device(0)

@@ -177,6 +177,7 @@ ss_status ctx_guard(ss_ctx* c, F&& f) {
     return SS_E_BACKEND;
   }
   try {
+    tsb::DeviceScope on(c->dg ? c->dg->device() : c->host->device());
     f();
     return SS_OK;
   } catch (const tsb::Error& e) {
@@ -330,6 +331,7 @@ ss_status open_impl(const ss_desc* d, const ss_budget* budget, const ss_plan* pl
     need(!plan || tsb::same_budget(plan->p.budget, bb), "ss_open: the plan was made with another budget");
     const tsb::Plan p = plan ? plan->p : tsb::plan_make(d->d, bb, {});
     need(o.forward_mode == SS_FORWARD_HOST || o.forward_mode == SS_FORWARD_DEVICE_GATED, "ss_open: unknown forward_mode");
+    tsb::DeviceScope on(o.device);  // the open runs on the context's device; the caller's comes back after
     if (o.forward_mode == SS_FORWARD_DEVICE_GATED) {
       auto dg = tsb::open_dg_context(d->d, p, o, peer);
       *out = new ss_ctx{nullptr, std::move(dg)};
@@ -346,7 +348,11 @@ ss_status open_impl(const ss_desc* d, const ss_budget* budget, const ss_plan* pl
 ss_status ss_open(const ss_desc* d, const ss_budget* budget, const ss_plan* plan, const ss_options* opt, ss_ctx** out) {
   return open_impl(d, budget, plan, opt, nullptr, out);
 }
-void ss_close(ss_ctx* c) { delete c; }
+void ss_close(ss_ctx* c) {
+  if (!c) return;
+  tsb::DeviceScope on(c->dg ? c->dg->device() : c->host->device());
+  delete c;
+}
 int ss_source_direct(const ss_ctx* c, int source) {
   if (!c) return -1;
   if (c->dg) return source < 0 || source >= c->dg->n_sources() ? -1 : c->dg->source_direct(source) ? 1 : 0;

@@ -13,10 +13,24 @@
 
 namespace tsb {
 
+// Makes `device` the calling thread's current CUDA device for the scope and puts the caller's back on exit, so no
+// ss_* call leaves the engine thread on another device than it had (a failed switch shows in the calls that follow).
+class DeviceScope {
+ public:
+  explicit DeviceScope(int device);
+  ~DeviceScope();
+  DeviceScope(const DeviceScope&) = delete;
+  DeviceScope& operator=(const DeviceScope&) = delete;
+
+ private:
+  int prev_ = -1;
+};
+
 class DgContext {
  public:
   virtual ~DgContext() = default;
   virtual bool poisoned() const = 0;
+  virtual int device() const = 0;  // the CUDA device the context lives on
   virtual void poison() = 0;
   virtual int n_sources() const = 0;
   virtual bool source_direct(int i) const = 0;
@@ -64,6 +78,7 @@ class HostContext {
  public:
   virtual ~HostContext() = default;
   virtual bool poisoned() const = 0;
+  virtual int device() const = 0;  // the CUDA device the context lives on
   virtual void poison() = 0;
   virtual int n_sources() const = 0;
   virtual bool source_direct(int i) const = 0;

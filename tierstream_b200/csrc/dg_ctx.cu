@@ -734,6 +734,7 @@ class CudaDgContext final : public DgContext {
 
   bool poisoned() const override { return poisoned_; }
   void poison() override { poisoned_ = true; }
+  int device() const override { return o_.device; }
   int n_sources() const override { return int(files_.size()); }
   bool source_direct(int i) const override { return files_[size_t(i)]->direct(); }
   int gated_index(int layer) const override {
@@ -1556,6 +1557,19 @@ class CudaDgContext final : public DgContext {
 };
 
 }  // namespace
+
+DeviceScope::DeviceScope(int device) {
+  int cur = -1;
+  if (cudaGetDevice(&cur) != cudaSuccess) {
+    (void)cudaGetLastError();
+    cur = -1;
+  }
+  if (cur != device && cudaSetDevice(device) == cudaSuccess) prev_ = cur;
+  else (void)cudaGetLastError();
+}
+DeviceScope::~DeviceScope() {
+  if (prev_ >= 0) cudaSetDevice(prev_);
+}
 
 std::unique_ptr<DgContext> open_dg_context(const Desc& d, const Plan& p, const ss_options& o, const PeerTier* peer) {
   require(o.backend == SS_BACKEND_CUDA, SS_E_UNSUPPORTED,

@@ -82,6 +82,7 @@ class HostCtx final : public HostContext {
 
   bool poisoned() const override { return poisoned_; }
   void poison() override { poisoned_ = true; }
+  int device() const override { return o_.device; }
   int n_sources() const override { return int(files_.size()); }
   bool source_direct(int i) const override { return files_[size_t(i)]->direct(); }
 
@@ -581,6 +582,7 @@ class HostCtx final : public HostContext {
   }
   // Reader thread: the unit's file bytes into a staging buffer (hash-checked with verify_hash), then to its slot.
   void worker() {
+    if (cudaSetDevice(o_.device) != cudaSuccess) (void)cudaGetLastError();  // its copies run on the context's device
     for (;;) {
       JobPtr j;
       {

@@ -11,6 +11,7 @@
 #include <string>
 #include <thread>
 
+#include "ctx.hpp"
 #include "errors.hpp"
 #include "kernels.hpp"
 #include "peer.hpp"
@@ -94,13 +95,13 @@ PeerStore::PeerStore(const Desc& d, const std::vector<int32_t>& owner, int32_t r
           "peer tier: the owner map has " + std::to_string(owner.size()) + " keys, the descriptor " +
               std::to_string(gk.keys()));
   require(rank >= 0, SS_E_INVALID, "peer tier: negative rank");
+  DeviceScope on(device);  // the caller's current device comes back on return
   std::vector<std::pair<uint32_t, uint32_t>> mine;  // (gated ordinal, unit), key order
   for (uint32_t g = 0; g + 1 < gk.base.size(); ++g)
     for (uint32_t u = 0; u < gk.base[g + 1] - gk.base[g]; ++u)
       if (owner[gk.base[g] + u] == rank) mine.push_back({g, u});
   units_ = mine.size();
   bytes_ = units_ * gk.unit_bytes;
-  ck(cudaSetDevice(device), "cudaSetDevice (peer store)");
   if (!bytes_) return;
   ck(cudaMalloc(reinterpret_cast<void**>(&base_), size_t(bytes_)), "cudaMalloc (peer store)");
   try {

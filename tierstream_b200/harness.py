@@ -54,6 +54,7 @@ class DgRun:
         o.verify_hash = 1 if verify else 0
         o.dg_wait_timeout_ms = timeout_ms
         o.dg_inclusive_blocks = inclusive
+        o.device = torch.cuda.current_device()  # the context lives on the engine's device
         self.ctx = runtime.DgContext(self.desc, self.plan, o, peer=peer)
         self.stream = torch.cuda.Stream()
         self.ids_pin = torch.zeros(G * max_ids, dtype=torch.int32).pin_memory()
