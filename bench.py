@@ -7,7 +7,10 @@ exclusive tiers; batch-1 decode with top-2 Zipf(1.1) routes, one token = one ste
 (begin; per layer export -> wait -> the engine's reader of the two routed experts; end), ss_end.
 
 Printed metric: expert-miss stream GB/s = bytes landed by the miss service (demand + prefetch copies) per second of
-decode, aggregated over ranks (N > 1 runs N independent replicas, "replicas only": the config fits one GPU).
+decode, aggregated over ranks. N > 1 (one process per GPU) runs the peer tier by default ("mixtral-8x7b-dg-peer"):
+each rank decodes its own trace, every expert is owned by one rank's HBM store (owners planned from the ranks' summed
+routing counts, one NCCL all-reduce), and a miss is copied from its owner's store over NVLink (or from the rank's own
+store) instead of pinned RAM; `--tier pinned` runs N independent pinned-RAM replicas instead.
 `value` is device time (CUDA events on the engine stream) with the routed ids already in HBM; `e2e` is the same steps
 through the public ABI with the ids copied from pinned host memory and the readers' results copied back each step,
 timed by the host clock. `--impl reference` times the reference's own DgCore (compiled from its sources) with a host
@@ -49,10 +52,11 @@ def args_():
     p.add_argument("--spare", type=int, default=SPARE, help="spare slots per layer (dynamic_slots_per_layer)")
     p.add_argument("--cpu-sample-tokens", type=int, default=6)
     p.add_argument("--no-cpu-baseline", action="store_true")
-    p.add_argument("--peer", action="store_true",
-                   help="the peer tier: every expert owned by one rank's HBM store (owners planned from the ranks' "
-                        "summed routing counts, one all-reduce); a miss is copied from its owner's store (NVLink for "
-                        "a peer, HBM for the rank's own) instead of pinned RAM")
+    p.add_argument("--tier", default="auto", choices=["auto", "pinned", "peer"],
+                   help="where non-resident experts live: pinned RAM, or the peer tier (every expert owned by one "
+                        "rank's HBM store, owners planned from the ranks' summed routing counts by one all-reduce; a "
+                        "miss is copied from its owner's store, NVLink for a peer, HBM for the rank's own); auto = "
+                        "pinned at one GPU, peer at several")
     p.add_argument("--peer-copy", default="kernel", choices=["kernel", "ce"],
                    help="peer tier mover: the land kernel's SM loads or the copy engines")
     return p.parse_args()
@@ -135,6 +139,15 @@ def h2d_peak(torch):
     return n / (best / 1e3) / 1e9
 
 
+def hbm_copy_peak():
+    """The measured HBM copy rate (GB/s copied; MEASURED_PEAKS.json counts read + write), else the pool's fallback."""
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["hbm_gbs"]) / 2
+    except (OSError, KeyError, ValueError):
+        return 6650.0 / 2
+
+
 def inclusive_of(a):
     return LAYERS * UNITS - RESIDENTS if a.inclusive < 0 else a.inclusive
 
@@ -196,6 +209,7 @@ def main():
     from tierstream_b200 import abi, harness, synth
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
+    a.peer = a.tier == "peer" or (a.tier == "auto" and world > 1)
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
@@ -239,7 +253,8 @@ def main():
         # input buffer, no host copy
         trace_dev = torch.from_numpy(ids[a.warmup:].reshape(a.steps, -1).copy()).cuda()
         s0 = run.ctx.stats()
-        j0 = json.loads(run.ctx.stats_json())["dg"]
+        f0 = json.loads(run.ctx.stats_json())
+        j0 = f0["dg"]
         clocks = Clocks(local)
         barrier()
         torch.cuda.synchronize()
@@ -257,7 +272,10 @@ def main():
         clk = clocks.stop()
         dev_ms = e0.elapsed_time(e1)
         s1 = run.ctx.stats()
-        j1 = json.loads(run.ctx.stats_json())["dg"]
+        f1 = json.loads(run.ctx.stats_json())
+        j1 = f1["dg"]
+        peer_units = f1["peer"]["peer_units"] - f0["peer"]["peer_units"]
+        self_units = f1["peer"]["self_units"] - f0["peer"]["self_units"]
         units_moved = (s1["fetched"] - s0["fetched"]) + (s1["prefetched"] - s0["prefetched"])
         moved = units_moved * unit
         dma_ms = j1["dma_ms_total"] - j0["dma_ms_total"]
@@ -332,12 +350,20 @@ def main():
         # rank's own store; no pinned RAM is allocated
         line["config"].update({"workload": "mixtral-8x7b-dg-peer", "parallelism": "peer tier x%d" % world,
                                "peer_copy": a.peer_copy})
-        line["peer"] = peer_stats
+        line["peer"] = dict(peer_stats, timed_peer_units=peer_units, timed_self_units=self_units)
+        # the demand stream moves peer units over NVLink and own-store units inside HBM in the same time: the peak is
+        # the rate of an ideal mover doing both, each at its measured rate
+        hbm_copy = hbm_copy_peak()
+        ideal_s = (peer_units * unit / 770e9) + (self_units * unit / (hbm_copy * 1e9))
+        peak_mix = (peer_units + self_units) * unit / ideal_s / 1e9 if ideal_s > 0 else None
         line["roofline"].update({
-            "bound": "nvlink", "kernel": "miss service from the stores (peer pulls over NVLink + own-store copies)",
-            "peak": 770.0, "frac": round(achieved / 770.0, 4) if achieved else None,
-            "peak_source": "peer copy 770 GB/s per direction, measured on this pool (MEASURED_PEAKS.json has no "
-                           "NVLink figure); own-store copies (HBM) are in the same time"})
+            "bound": "nvlink+hbm", "kernel": "miss service from the stores (peer pulls over NVLink + own-store copies)",
+            "peak": round(peak_mix, 3) if peak_mix else None,
+            "frac": round(achieved / peak_mix, 4) if achieved and peak_mix else None,
+            "peak_source": "blend of the peer copy 770 GB/s per direction measured on this pool (MEASURED_PEAKS.json "
+                           "has no NVLink figure) for the %d units pulled from peers and the measured HBM copy rate "
+                           "(MEASURED_PEAKS.json hbm_gbs / 2 = %.1f GB/s) for the %d units copied from the rank's own "
+                           "store, rank 0's timed tokens" % (peer_units, hbm_copy, self_units)})
     if not a.no_cpu_baseline and world == 1:
         smp = a.cpu_sample_tokens
         mv, dt = reference_sample(synth.zipf_trace(smp, LAYERS, UNITS, TOP_K, s=ZIPF, seed=1), smp, a)
