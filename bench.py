@@ -32,6 +32,14 @@ sys.path.insert(0, ROOT)
 LAYERS, UNITS, PART = 32, 8, 33030144
 TOP_K, ZIPF, RESIDENTS, SPARE = 2, 1.1, 102, 1
 METRIC = "expert-miss stream GB/s (device-gated decode, Mixtral-8x7B-shaped MoE)"
+WORKLOAD, MODEL_FILE = "mixtral-8x7b-dg", "tsb-bench-mixtral-dg.bin"
+# BASELINE configs[4] (C5): 94 layers x 128 experts of 3 x 12,582,912 B (4096 x 1536 bf16), top-8 Zipf(1.2), one
+# decode stream per GPU with its own seed, every expert owned by one GPU's store (454 GB over the GPUs' HBM, so 4 or
+# more GPUs); each GPU keeps its 12 most popular experts per layer resident (1,128 units, 42.6 GB). The stores are
+# written on the device from the model's byte generator (the model file is sparse: 454 GB is more than host RAM).
+QWEN3 = dict(LAYERS=94, UNITS=128, PART=12582912, TOP_K=8, ZIPF=1.2, RESIDENTS=94 * 12,
+             METRIC="expert-miss stream GB/s (device-gated decode, Qwen3-235B-A22B-shaped MoE, peer tier)",
+             WORKLOAD="qwen3-235b-a22b-peer", MODEL_FILE="tsb-bench-qwen3-peer.bin")
 
 
 def args_():
@@ -57,6 +65,12 @@ def args_():
                         "rank's HBM store, owners planned from the ranks' summed routing counts by one all-reduce; a "
                         "miss is copied from its owner's store, NVLink for a peer, HBM for the rank's own); auto = "
                         "pinned at one GPU, peer at several")
+    p.add_argument("--workload", default="mixtral-8x7b-dg", choices=["mixtral-8x7b-dg", "qwen3-235b-a22b-peer"],
+                   help="mixtral-8x7b-dg: BASELINE configs[1] (default); qwen3-235b-a22b-peer: configs[4], the peer "
+                        "tier on 4 or more GPUs")
+    p.add_argument("--layers", type=int, default=0,
+                   help="qwen3 only: fewer layers than the 94 of the config, for trying the path on fewer GPUs (the "
+                        "line then names the layer count; not the config's number)")
     p.add_argument("--peer-copy", default="kernel", choices=["kernel", "ce"],
                    help="peer tier mover: the land kernel's SM loads or the copy engines")
     return p.parse_args()
@@ -71,7 +85,18 @@ def resident_keys(seed):
 
 def model_path():
     from tierstream_b200 import harness
-    return os.path.join(harness.model_dir(), "tsb-bench-mixtral-dg.bin")
+    return os.path.join(harness.model_dir(), MODEL_FILE)
+
+
+def configure(a):
+    """Sets the workload's shape (the module constants)."""
+    if a.workload == "qwen3-235b-a22b-peer":
+        g = globals()
+        g.update(QWEN3)
+        if a.layers:
+            g["LAYERS"] = a.layers
+            g["RESIDENTS"] = a.layers * 12
+            g["MODEL_FILE"] = "tsb-bench-qwen3-peer-%d.bin" % a.layers
 
 
 class Clocks:
@@ -189,7 +214,7 @@ def run_reference(a):
     line = {"impl": "reference", "metric": METRIC, "value": round(v, 3), "unit": "GB/s", "n_gpus": a.gpus,
             "steps": a.steps, "warmup": a.warmup, "ms_per_step": round(dt * 1e3 / a.steps, 3),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u8", "data": "synthetic",
-            "config": {"workload": "mixtral-8x7b-dg", "layers": LAYERS, "experts": UNITS, "part_bytes": PART,
+            "config": {"workload": WORKLOAD, "layers": LAYERS, "experts": UNITS, "part_bytes": PART,
                        "top_k": TOP_K, "zipf": ZIPF, "residents": RESIDENTS, "tokens": a.steps},
             "cpu_baseline": {"value": round(v, 3), "unit": "GB/s", "cores": 1, "kind": "reference",
                              "sample": "%d tokens of the trace through the reference DgCore (oracle/_ref) with a "
@@ -202,6 +227,7 @@ def run_reference(a):
 
 def main():
     a = args_()
+    configure(a)
     if a.impl == "reference":
         return run_reference(a)
     os.environ["TSB_COPY_MODE"] = a.copy_mode
@@ -224,8 +250,14 @@ def main():
             dist.barrier()
 
     model = synth.Model(model_path(), LAYERS, UNITS, [PART] * 3, seed=0, top_k=TOP_K)
+    qwen = a.workload == "qwen3-235b-a22b-peer"
+    if qwen and not a.peer:
+        raise SystemExit("qwen3-235b-a22b-peer runs the peer tier only (its experts do not fit pinned RAM)")
     if rank == 0:
-        model.write()
+        if qwen:
+            model.create_sparse()
+        else:
+            model.write()
     barrier()
     peak = h2d_peak(torch) if rank == 0 and not a.peer else None
     ids = synth.zipf_trace(a.warmup + a.steps, LAYERS, UNITS, TOP_K, s=ZIPF, seed=1 + rank)
@@ -238,9 +270,26 @@ def main():
         # the planner's input: this rank's routing counts over a calibration window of its own trace distribution
         cal = synth.zipf_trace(64, LAYERS, UNITS, TOP_K, s=ZIPF, seed=1001 + rank)
         counts = np.bincount((np.arange(LAYERS)[None, :, None] * UNITS + cal).reshape(-1), minlength=LAYERS * UNITS)
+        filler = None
+        if qwen:
+            def filler(store, owner):
+                # every owned unit written on the device from the model's byte generator, in store order; the first
+                # one checked against the host generator
+                keys = np.nonzero(owner == rank)[0]
+                offs = np.array([model.unit_offset(int(k) // UNITS, int(k) % UNITS) for k in keys], dtype=np.uint64)
+                if not keys.size:
+                    return
+                s = torch.cuda.Stream()
+                rc = abi.load_engine().tse_fill_units_device(model.seed, offs.ctypes.data_as(C.POINTER(C.c_uint64)),
+                                                             keys.size, model.unit_bytes, store.base, s.cuda_stream)
+                assert rc == 0, "device fill failed: %d" % rc
+                s.synchronize()
+                first = peer_mod.read_device(store.base, model.unit_bytes)
+                k0 = int(keys[0])
+                assert np.array_equal(first, model.unit_bytes_of(k0 // UNITS, k0 % UNITS)), "store fill differs"
         setup = peer_mod.PeerSetup(runtime.Desc(model.desc()), counts, dist, world, rank, local, verify=False,
                                    copy=1 if a.peer_copy == "ce" else 0,
-                                   collective_device=torch.device("cuda", local) if dist else None)
+                                   collective_device=torch.device("cuda", local) if dist else None, filler=filler)
     run = harness.DgRun(model, resident_keys=resident_keys(1 + rank), spare_per_layer=a.spare, max_ids=TOP_K,
                         diag=True, test_hooks=False, mode=1, slices=128, wb_defer=a.wb_defer, wb_stream=a.wb_stream,
                         inclusive=inclusive, peer=setup.tier if setup else None)
@@ -325,7 +374,7 @@ def main():
         "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": world, "steps": a.steps,
         "warmup": a.warmup, "ms_per_step": round(dev_ms_max / a.steps, 3), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "u8", "data": "synthetic (seeded random bytes and Zipf routes)",
-        "config": {"workload": "mixtral-8x7b-dg", "layers": LAYERS, "experts": UNITS, "part_bytes": PART,
+        "config": {"workload": WORKLOAD, "layers": LAYERS, "experts": UNITS, "part_bytes": PART,
                    "unit_bytes": unit, "top_k": TOP_K, "zipf": ZIPF, "residents": RESIDENTS,
                    "spare_slots_per_layer": SPARE, "parallelism": "replicas" if world > 1 else "single",
                    "copy_mode": a.copy_mode, "l2": "inputs larger than L2 (99 MB units, 10 GB arena)"},
@@ -348,7 +397,8 @@ def main():
     if a.peer:
         # every expert lives in one rank's store: a miss is an NVLink pull from a peer or an HBM copy from the
         # rank's own store; no pinned RAM is allocated
-        line["config"].update({"workload": "mixtral-8x7b-dg-peer", "parallelism": "peer tier x%d" % world,
+        line["config"].update({"workload": WORKLOAD if qwen else "mixtral-8x7b-dg-peer",
+                               "parallelism": "peer tier x%d" % world,
                                "peer_copy": a.peer_copy})
         line["peer"] = dict(peer_stats, timed_peer_units=peer_units, timed_self_units=self_units)
         # the demand stream moves peer units over NVLink and own-store units inside HBM in the same time: the peak is

@@ -108,6 +108,10 @@ SS_API ss_status tsb_peer_index(const int32_t* owner, uint32_t keys, uint32_t wo
  * verify and descriptor hashes, checked on the device (K3). An empty store (no unit owned) has a NULL base. */
 SS_API ss_status tsb_peer_store_create(const ss_desc* d, const int32_t* owner, uint32_t keys, int32_t rank,
                                        int device, int verify, tsb_peer_store** out);
+/* The same store allocated only, for a caller that writes the units itself (its own loader): unit i of the store
+ * (tsb_peer_index) at base + i x unit_bytes, its parts back to back in descriptor order; nothing is read or checked. */
+SS_API ss_status tsb_peer_store_alloc(const ss_desc* d, const int32_t* owner, uint32_t keys, int32_t rank, int device,
+                                      tsb_peer_store** out);
 SS_API void tsb_peer_store_free(tsb_peer_store* s);
 SS_API void* tsb_peer_store_base(const tsb_peer_store* s);
 SS_API uint64_t tsb_peer_store_bytes(const tsb_peer_store* s);

@@ -206,6 +206,7 @@ _PROTOS = {
     "tsb_peer_plan": (C.c_int, [P(u64), u32, u32, P(u64), P(C.c_int32)]),
     "tsb_peer_index": (C.c_int, [P(C.c_int32), u32, u32, P(i64), P(u64)]),
     "tsb_peer_store_create": (C.c_int, [vp, P(C.c_int32), u32, C.c_int32, C.c_int, C.c_int, P(vp)]),
+    "tsb_peer_store_alloc": (C.c_int, [vp, P(C.c_int32), u32, C.c_int32, C.c_int, P(vp)]),
     "tsb_peer_store_free": (None, [vp]),
     "tsb_peer_store_base": (vp, [vp]),
     "tsb_peer_store_bytes": (u64, [vp]),
@@ -227,6 +228,7 @@ _ENGINE_PROTOS = {
     "tse_destroy": (C.c_int, [vp]),
     "tse_read_units": (C.c_int, [vp, u32, vp, u32, vp, u32, C.c_int, vp]),
     "tse_fill_bytes": (None, [u64, u64, u64, vp, u32]),
+    "tse_fill_units_device": (C.c_int, [u64, P(u64), u32, u64, vp, vp]),
     "tse_read_table": (C.c_int, [vp, vp, u32, u64, vp, u32, vp]),
 }
 

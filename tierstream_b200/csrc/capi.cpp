@@ -651,6 +651,17 @@ ss_status tsb_peer_store_create(const ss_desc* d, const int32_t* owner, uint32_t
     *out = s.release();
   });
 }
+ss_status tsb_peer_store_alloc(const ss_desc* d, const int32_t* owner, uint32_t keys, int32_t rank, int device,
+                               tsb_peer_store** out) {
+  return guard([&] {
+    need(d && owner && out, "tsb_peer_store_alloc: null argument");
+    *out = nullptr;
+    auto s = std::make_unique<tsb_peer_store>();
+    s->s = std::make_unique<tsb::PeerStore>(d->d, std::vector<int32_t>(owner, owner + keys), rank, device, false,
+                                            false);
+    *out = s.release();
+  });
+}
 void tsb_peer_store_free(tsb_peer_store* s) { delete s; }
 void* tsb_peer_store_base(const tsb_peer_store* s) { return s && s->s ? s->s->base() : nullptr; }
 uint64_t tsb_peer_store_bytes(const tsb_peer_store* s) { return s && s->s ? s->s->bytes() : 0; }

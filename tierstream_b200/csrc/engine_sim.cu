@@ -200,6 +200,41 @@ __attribute__((visibility("default"))) void tse_fill_bytes(uint64_t file_id, uin
   for (auto& t : th) t.join();
 }
 
+// The same byte stream written on the device: n bytes of file `file_id` from position `first` into dst (HBM), for a
+// store the caller fills itself (tsb_peer_store_alloc) without a model file on disk.
+__global__ void fill_bytes_kernel(uint64_t file_id, uint64_t first, uint64_t n, uint8_t* __restrict__ dst) {
+  const uint64_t stride = uint64_t(gridDim.x) * blockDim.x * 8;
+  for (uint64_t j = (uint64_t(blockIdx.x) * blockDim.x + threadIdx.x) * 8; j < n; j += stride) {
+    uint64_t word = 0;
+    const uint64_t m = n - j < 8 ? n - j : 8;
+    for (uint64_t k = 0; k < m; ++k) {
+      const uint64_t i = first + j + k;
+      uint64_t x = (i + 1) * 0x9E3779B97F4A7C15ULL ^ (file_id + 7) * 0xC2B2AE3D27D4EB4FULL;
+      x ^= x >> 29;
+      x *= 0xBF58476D1CE4E5B9ULL;
+      x ^= x >> 32;
+      word |= uint64_t(uint8_t(x)) << (8 * k);
+    }
+    if (m == 8 && ((reinterpret_cast<uintptr_t>(dst + j) & 7u) == 0)) {
+      *reinterpret_cast<uint64_t*>(dst + j) = word;
+    } else {
+      for (uint64_t k = 0; k < m; ++k) dst[j + k] = uint8_t(word >> (8 * k));
+    }
+  }
+}
+
+// n units: unit i's bytes (unit_bytes from file position offsets[i]) into dst + i * unit_bytes, on `stream`.
+__attribute__((visibility("default"))) int tse_fill_units_device(uint64_t file_id, const uint64_t* offsets, uint32_t n,
+                                                                 uint64_t unit_bytes, void* dst, void* stream) {
+  for (uint32_t i = 0; i < n; ++i) {
+    fill_bytes_kernel<<<592, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+        file_id, offsets[i], unit_bytes, static_cast<uint8_t*>(dst) + uint64_t(i) * unit_bytes);
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return int(e);
+  }
+  return 0;
+}
+
 __attribute__((visibility("default"))) int tse_launch(void* exec, void* stream) {
   return int(cudaGraphLaunch(static_cast<cudaGraphExec_t>(exec), static_cast<cudaStream_t>(stream)));
 }

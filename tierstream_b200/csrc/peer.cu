@@ -87,7 +87,7 @@ std::vector<int64_t> store_index(const std::vector<int32_t>& owner, uint32_t wor
   return index;
 }
 
-PeerStore::PeerStore(const Desc& d, const std::vector<int32_t>& owner, int32_t rank, int device, bool verify)
+PeerStore::PeerStore(const Desc& d, const std::vector<int32_t>& owner, int32_t rank, int device, bool verify, bool fill)
     : device_(device) {
   const auto t0 = std::chrono::steady_clock::now();
   const GatedKeys gk = gated_keys(d);
@@ -104,6 +104,10 @@ PeerStore::PeerStore(const Desc& d, const std::vector<int32_t>& owner, int32_t r
   bytes_ = units_ * gk.unit_bytes;
   if (!bytes_) return;
   ck(cudaMalloc(reinterpret_cast<void**>(&base_), size_t(bytes_)), "cudaMalloc (peer store)");
+  if (!fill) {
+    fill_s_ = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+    return;
+  }
   try {
     std::vector<std::unique_ptr<SourceFile>> files;
     for (const Source& s : d.sources) files.push_back(std::make_unique<SourceFile>(s.path, s.align, false));

@@ -49,17 +49,18 @@ struct PeerTier {
   bool owned(uint32_t key) const { return owner[key] >= 0; }
 };
 
-// This rank's store: cudaMalloc'd on `device`, filled from the descriptor's sources, checked on the device against
-// the descriptor's hashes (K3) when verify is set and the descriptor has them.
 // CUDA IPC for the stores: the handle of a store (64 bytes), a mapping of another process's store on `device` with
 // peer access enabled, and its release.
 void ipc_export(const void* base, void* handle);
 void* ipc_map(const void* handle, int device);
 void ipc_unmap(void* base);
 
+// This rank's store: cudaMalloc'd on `device`, filled from the descriptor's sources, checked on the device against
+// the descriptor's hashes (K3) when verify is set and the descriptor has them; with fill = false only allocated (the
+// caller writes every unit's bytes).
 class PeerStore {
  public:
-  PeerStore(const Desc& d, const std::vector<int32_t>& owner, int32_t rank, int device, bool verify);
+  PeerStore(const Desc& d, const std::vector<int32_t>& owner, int32_t rank, int device, bool verify, bool fill = true);
   ~PeerStore();
   PeerStore(const PeerStore&) = delete;
   PeerStore& operator=(const PeerStore&) = delete;

@@ -42,11 +42,16 @@ def store_index(owner, world):
 class Store:
     """This rank's store: the units it owns, in its GPU's HBM (tsb_peer_store_create)."""
 
-    def __init__(self, desc, owner, rank, device=0, verify=True):
+    def __init__(self, desc, owner, rank, device=0, verify=True, fill=True):
+        """fill = False: allocated only (tsb_peer_store_alloc); the caller writes every unit."""
         owner = np.ascontiguousarray(owner, dtype=np.int32)
         self.h = C.c_void_p()
-        abi.check(abi.load().tsb_peer_store_create(desc.h, owner.ctypes.data_as(C.POINTER(C.c_int32)), owner.size,
-                                                   rank, device, 1 if verify else 0, C.byref(self.h)))
+        op = owner.ctypes.data_as(C.POINTER(C.c_int32))
+        if fill:
+            abi.check(abi.load().tsb_peer_store_create(desc.h, op, owner.size, rank, device, 1 if verify else 0,
+                                                       C.byref(self.h)))
+        else:
+            abi.check(abi.load().tsb_peer_store_alloc(desc.h, op, owner.size, rank, device, C.byref(self.h)))
         self.base = abi.load().tsb_peer_store_base(self.h) or 0
         self.bytes = int(abi.load().tsb_peer_store_bytes(self.h))
 
@@ -65,6 +70,16 @@ class Store:
 
     def __del__(self):
         self.close()
+
+
+def read_device(ptr, nbytes):
+    """nbytes of device memory at ptr (an address on the current device) as a host numpy array."""
+    import torch
+
+    class _View:
+        __cuda_array_interface__ = {"shape": (nbytes,), "typestr": "|u1", "data": (ptr, True), "version": 3}
+
+    return torch.as_tensor(_View(), device="cuda").cpu().numpy()
 
 
 def map_store(handle, device):
@@ -125,14 +140,17 @@ class PeerSetup:
     Close it after the context that uses it."""
 
     def __init__(self, desc, local_counts, dist, world, rank, device, cap_units=None, verify=True, copy=0,
-                 collective_device=None):
+                 collective_device=None, filler=None):
+        """filler(store, owner): writes the rank's store itself (the store is then only allocated by the library)."""
         if dist is None:  # one rank: nothing to exchange
             assert world == 1 and rank == 0
             self.counts = np.ascontiguousarray(local_counts, dtype=np.uint64)
         else:
             self.counts = all_reduce_counts(local_counts, dist, collective_device)
         self.owner = plan_owners(self.counts, world, cap_units)
-        self.store = Store(desc, self.owner, rank, device, verify)
+        self.store = Store(desc, self.owner, rank, device, verify, fill=filler is None)
+        if filler is not None:
+            filler(self.store, self.owner)
         handles = ([self.store.handle()] if dist is None else
                    all_gather_handles(self.store.handle(), dist, world, collective_device))
         self.mapped = []

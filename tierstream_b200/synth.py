@@ -52,6 +52,13 @@ class Model:
                 pos += n
         os.replace(self.path + ".tmp", self.path)
 
+    def create_sparse(self):
+        """A model file of the right size whose bytes are never read (the peer tier's stores are filled on the device
+        from the same generator): a sparse file, no data written."""
+        if not (os.path.exists(self.path) and os.path.getsize(self.path) == self.file_bytes):
+            with open(self.path, "wb") as f:
+                f.truncate(self.file_bytes)
+
     def unit_bytes_of(self, layer, unit):
         """The unit's engine bytes (its parts back to back) as numpy uint8."""
         out = np.empty(self.unit_bytes, dtype=np.uint8)
