@@ -77,7 +77,7 @@ def read_device(ptr, nbytes):
     import torch
 
     class _View:
-        __cuda_array_interface__ = {"shape": (nbytes,), "typestr": "|u1", "data": (ptr, True), "version": 3}
+        __cuda_array_interface__ = {"shape": (nbytes,), "typestr": "|u1", "data": (ptr, False), "version": 3}
 
     return torch.as_tensor(_View(), device="cuda").cpu().numpy()
 
