@@ -35,9 +35,10 @@ METRIC = "expert-miss stream GB/s (device-gated decode, Mixtral-8x7B-shaped MoE)
 WORKLOAD, MODEL_FILE = "mixtral-8x7b-dg", "tsb-bench-mixtral-dg.bin"
 # BASELINE configs[4] (C5): 94 layers x 128 experts of 3 x 12,582,912 B (4096 x 1536 bf16), top-8 Zipf(1.2), one
 # decode stream per GPU with its own seed, every expert owned by one GPU's store (454 GB over the GPUs' HBM, so 4 or
-# more GPUs); each GPU keeps its 12 most popular experts per layer resident (1,128 units, 42.6 GB). The stores are
-# written on the device from the model's byte generator (the model file is sparse: 454 GB is more than host RAM).
-QWEN3 = dict(LAYERS=94, UNITS=128, PART=12582912, TOP_K=8, ZIPF=1.2, RESIDENTS=94 * 12,
+# more GPUs); each GPU keeps its 8 most popular experts per layer resident (752 units, 28.4 GB) and 4 spare slots
+# per layer for the misses (a top-8 layer misses several experts at once). The stores are written on the device from
+# the model's byte generator (the model file is sparse: 454 GB is more than host RAM).
+QWEN3 = dict(LAYERS=94, UNITS=128, PART=12582912, TOP_K=8, ZIPF=1.2, RESIDENTS=94 * 8, SPARE=4,
              METRIC="expert-miss stream GB/s (device-gated decode, Qwen3-235B-A22B-shaped MoE, peer tier)",
              WORKLOAD="qwen3-235b-a22b-peer", MODEL_FILE="tsb-bench-qwen3-peer.bin")
 
@@ -57,7 +58,8 @@ def args_():
                    help="ss_options.dg_inclusive_blocks: device units keeping their pinned block as a clean copy "
                         "(an eviction is then a drop, no write-back); -1 = every pinned unit")
     p.add_argument("--wb-stream", type=int, default=1, help="ss_options.dg_wb_stream (the reference default 1)")
-    p.add_argument("--spare", type=int, default=SPARE, help="spare slots per layer (dynamic_slots_per_layer)")
+    p.add_argument("--spare", type=int, default=0,
+                   help="spare slots per layer (dynamic_slots_per_layer); 0 = the workload's (1 Mixtral, 4 Qwen3)")
     p.add_argument("--cpu-sample-tokens", type=int, default=6)
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--tier", default="auto", choices=["auto", "pinned", "peer"],
@@ -95,7 +97,7 @@ def configure(a):
         g.update(QWEN3)
         if a.layers:
             g["LAYERS"] = a.layers
-            g["RESIDENTS"] = a.layers * 12
+            g["RESIDENTS"] = a.layers * 8
             g["MODEL_FILE"] = "tsb-bench-qwen3-peer-%d.bin" % a.layers
 
 
@@ -228,6 +230,8 @@ def run_reference(a):
 def main():
     a = args_()
     configure(a)
+    if not a.spare:
+        a.spare = SPARE
     if a.impl == "reference":
         return run_reference(a)
     os.environ["TSB_COPY_MODE"] = a.copy_mode
@@ -376,8 +380,10 @@ def main():
         "scaling": "weak", "vs_baseline": None, "dtype": "u8", "data": "synthetic (seeded random bytes and Zipf routes)",
         "config": {"workload": WORKLOAD, "layers": LAYERS, "experts": UNITS, "part_bytes": PART,
                    "unit_bytes": unit, "top_k": TOP_K, "zipf": ZIPF, "residents": RESIDENTS,
-                   "spare_slots_per_layer": SPARE, "parallelism": "replicas" if world > 1 else "single",
-                   "copy_mode": a.copy_mode, "l2": "inputs larger than L2 (99 MB units, 10 GB arena)"},
+                   "spare_slots_per_layer": a.spare, "parallelism": "replicas" if world > 1 else "single",
+                   "copy_mode": a.copy_mode,
+                   "l2": "inputs larger than L2 (%.0f MB units, %.1f GB arena)" % (
+                       unit / 1e6, (RESIDENTS + a.spare * LAYERS + 2 * TOP_K + 1) * unit / 1e9)},
         "tokens_per_s": round(a.steps * world / (dev_ms_max / 1e3), 3),
         "misses_per_token": round(misses / a.steps, 3), "lookups_per_token": round(lookups / a.steps, 3),
         "e2e": {"value": round(e2e, 3), "unit": "GB/s", "h2d_bytes_per_step": LAYERS * TOP_K * 4,
