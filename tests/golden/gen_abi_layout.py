@@ -1,6 +1,6 @@
 """Writes tests/golden/abi_layout.json: the size and every field offset of the ABI's versioned structs, compiled
-against the reference's own include/strix_stream/ss.h (run where the reference checkout exists:
-python tests/golden/gen_abi_layout.py /root/reference/include)."""
+against the reference's own include/strix_stream/ss.h (run where the reference checkout exists, with its include
+directory as the argument; default: ../reference/include beside this repository)."""
 import json
 import os
 import re
@@ -59,4 +59,5 @@ def main(include_dir):
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference/include")
+    main(sys.argv[1] if len(sys.argv) > 1 else
+         os.path.join(os.path.dirname(os.path.dirname(HERE)), "..", "reference", "include"))

@@ -16,7 +16,9 @@ def _make(directory, extra=()):
 def build(oracle=True):
     _make(os.path.join(HERE, "csrc"))
     if oracle:
-        extra = [] if os.path.isdir("/root/reference/src") else ["REF=/nonexistent"]
+        # the reference checkout beside this repository, when present, for the reference harness
+        ref = os.path.normpath(os.path.join(ROOT, "..", "reference"))
+        extra = ["REF=" + ref] if os.path.isdir(os.path.join(ref, "src")) else ["REF=/nonexistent"]
         _make(os.path.join(ROOT, "oracle"), extra)
 
 
