@@ -166,6 +166,24 @@ def h2d_peak(torch):
     return n / (best / 1e3) / 1e9
 
 
+def miss_layer_path(ctx, layers):
+    """Where a missing layer's time goes, over the last timed token's layers that missed (means, microseconds):
+    export written -> seen by the service, the service's serve, the demand copies on the device, the wait kernel's
+    wait; and the layers counted."""
+    rows = [ctx.timeline(g) for g in range(layers)]
+    rows = [r for r in rows if r["misses"] > 0 and r["dma_ms"] >= 0]
+    if not rows:
+        return None
+
+    def mean(k, scale=1.0):
+        v = [r[k] * scale for r in rows if r[k] >= 0]
+        return round(sum(v) / len(v), 2) if v else None
+
+    return {"layers_with_misses": len(rows), "misses_per_layer": mean("misses"), "seen_us": mean("seen_us"),
+            "serve_us": mean("serve_us"), "copies_us": mean("dma_ms", 1000.0), "gpu_wait_us": mean("gpu_wait_us"),
+            "export_to_ready_us": mean("gpu_export_ready_us")}
+
+
 def hbm_copy_peak():
     """The measured HBM copy rate (GB/s copied; MEASURED_PEAKS.json counts read + write), else the pool's fallback."""
     try:
@@ -327,6 +345,7 @@ def main():
         s1 = run.ctx.stats()
         f1 = json.loads(run.ctx.stats_json())
         j1 = f1["dg"]
+        layer_path = miss_layer_path(run.ctx, LAYERS)
         peer_units = f1["peer"]["peer_units"] - f0["peer"]["peer_units"]
         self_units = f1["peer"]["self_units"] - f0["peer"]["self_units"]
         units_moved = (s1["fetched"] - s0["fetched"]) + (s1["prefetched"] - s0["prefetched"])
@@ -396,7 +415,7 @@ def main():
                                     "(MEASURED_PEAKS.json has no host-link figure)",
                      "algorithmic_bytes": moved, "device_ms": round(dma_ms, 3)},
         "gpu_launches": int(a.steps * (2 + 2 * LAYERS) + land_launches + a.steps * LAYERS),
-        "clocks": clk, "open_s": round(t_open, 2), "open": open_stats, "dg": dg,
+        "clocks": clk, "open_s": round(t_open, 2), "open": open_stats, "dg": dg, "miss_layer_path": layer_path,
         "options": {"wb_defer": a.wb_defer, "wb_stream": a.wb_stream, "spare_slots_per_layer": a.spare,
                     "inclusive_blocks": inclusive},
     }

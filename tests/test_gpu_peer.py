@@ -151,3 +151,37 @@ def test_two_gpus_exchange_and_pull(model, orc, tmp_path):
                                     spare_target=model.layers, order=list(r[rank]["resident"]), tokens=30, n_ids=2)
         t_ref, _ = oracle.ref_replay(cfg, ids)
         assert np.array_equal(r[rank]["table"], t_ref[-1]), "rank %d slot table differs" % rank
+
+
+def test_allocated_stores_written_on_the_device(model, orc, monkeypatch):
+    """Stores the library only allocates (tsb_peer_store_alloc), written by the caller: here by the model's byte
+    generator on the device (the benchmark's way to fill stores larger than host RAM). The decode then reads the
+    source bytes and the tables equal the reference replay, as with stores filled from the file."""
+    import ctypes as C
+
+    from tierstream_b200 import abi
+    monkeypatch.setenv("TSB_DG_DETERMINISTIC", "1")
+    m = model
+    ids = synth.zipf_trace(20, m.layers, m.units, 2, s=1.0, seed=23)
+    owner = peer.plan_owners(route_counts(m, ids[:8]), 2)
+    desc = runtime.Desc(m.desc())
+    stores = [peer.Store(desc, owner, r, 0, fill=False) for r in range(2)]
+    eng = abi.load_engine()
+    s = torch.cuda.Stream()
+    for r, st in enumerate(stores):
+        keys = np.nonzero(owner == r)[0]
+        offs = np.array([m.unit_offset(int(k) // m.units, int(k) % m.units) for k in keys], dtype=np.uint64)
+        assert eng.tse_fill_units_device(m.seed, offs.ctypes.data_as(C.POINTER(C.c_uint64)), keys.size, m.unit_bytes,
+                                         st.base, s.cuda_stream) == 0
+    s.synchronize()
+    k0 = int(np.nonzero(owner == 1)[0][0])
+    assert np.array_equal(peer.read_device(stores[1].base, m.unit_bytes),
+                          m.unit_bytes_of(k0 // m.units, k0 % m.units))
+    run = harness.DgRun(m, residents_per_layer=3, max_ids=2, peer=peer.Tier(2, 0, owner, [x.base for x in stores]))
+    try:
+        t_ref, _ = oracle.ref_replay(replay_cfg_for(run, m, ids.shape[0]), ids)
+        check_run(run, m, ids, expected_sums(m, orc), t_ref)
+    finally:
+        run.close()
+        for x in stores:
+            x.close()

@@ -131,6 +131,12 @@ class DgContext:
     def reset_open(self):
         abi.check(abi.load().ss_dg_reset_open(self.h))
 
+    def timeline(self, g):
+        """The last token's timeline of gated layer g (ss_dg_timeline; -1 where not measured)."""
+        t = abi.ss_dg_layer_timeline()
+        abi.check(abi.load().ss_dg_timeline_sized(self.h, g, C.byref(t), C.sizeof(t)))
+        return {n: getattr(t, n) for n, _ in t._fields_}
+
 
 class HostContext:
     """A host forward mode context (ss_open with forward_mode = SS_FORWARD_HOST)."""
