@@ -137,6 +137,19 @@ typedef struct tsb_peer_tier {
 SS_API ss_status tsb_open_peer(const ss_desc* d, const ss_budget* budget, const ss_plan* plan, const ss_options* opt,
                                const tsb_peer_tier* peer, ss_ctx** out);
 
+/* A re-plan (after a new all-reduce of routing counts and tsb_peer_plan): dst, allocated by tsb_peer_store_alloc for
+ * the new owners, is filled with its units from where they live now (old_owner, old_base[world]: every rank's current
+ * store as seen from this process), by the land kernel on `stream` (peers over NVLink, this rank's own store in HBM);
+ * returns after the copies landed. A unit unowned before cannot join this way (a new store reads it from its file).
+ * Outputs (may be NULL): units copied, of them from peers, bytes. */
+SS_API ss_status tsb_peer_store_migrate(tsb_peer_store* dst, const int32_t* old_owner, void* const* old_base,
+                                        uint32_t keys, uint32_t world, void* stream, uint64_t* moved_units,
+                                        uint64_t* moved_peer_units, uint64_t* moved_bytes);
+/* Between tokens: the context's owners and store addresses replaced by `peer` (the same world, rank and set of owned
+ * units; only owners change). Every copy that read the old stores has finished when it returns, so every rank may
+ * release its old stores once all ranks returned from this call. */
+SS_API ss_status tsb_dg_peer_retier(ss_ctx* c, const tsb_peer_tier* peer);
+
 #ifdef __cplusplus
 }
 #endif

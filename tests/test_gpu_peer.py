@@ -97,6 +97,50 @@ def test_emulated_two_ranks(model, orc, monkeypatch, copy, mixed):
             s.close()
 
 
+def test_replan_migrates_the_stores_mid_decode(model, orc, monkeypatch):
+    """A planning round between tokens: new owners from other counts, new stores filled from the current ones
+    (tsb_peer_store_migrate), the context switched to them (tsb_dg_peer_retier), the old stores freed. The decode
+    goes on reading the source bytes, and the tables keep equal to the reference replay of the whole trace (the
+    owners never enter the cache's decisions)."""
+    import torch as T
+    monkeypatch.setenv("TSB_DG_DETERMINISTIC", "1")
+    m = model
+    ids = synth.zipf_trace(30, m.layers, m.units, 2, s=1.0, seed=31)
+    a = peer.plan_owners(route_counts(m, ids[:10]), 2)
+    b = peer.plan_owners(route_counts(m, synth.zipf_trace(10, m.layers, m.units, 2, s=1.0, seed=99)), 2)
+    assert (a != b).sum() > 10
+    desc = runtime.Desc(m.desc())
+    old = [peer.Store(desc, a, r, 0, verify=True) for r in range(2)]
+    run = harness.DgRun(m, residents_per_layer=3, max_ids=2, peer=peer.Tier(2, 0, a, [x.base for x in old]))
+    new = []
+    try:
+        want = expected_sums(m, orc)
+        t_ref, _ = oracle.ref_replay(replay_cfg_for(run, m, ids.shape[0]), ids)
+        check_run(run, m, ids[:15], want, t_ref[:15])
+        s = T.cuda.Stream()
+        for r in range(2):
+            st = peer.Store(desc, b, r, 0, fill=False)
+            units, peer_units, nbytes = st.migrate_from(a, [x.base for x in old], s.cuda_stream)
+            assert units == (b == r).sum() and peer_units == ((b == r) & (a != r)).sum()
+            assert nbytes == units * m.unit_bytes
+            new.append(st)
+        run.ctx.retier(peer.Tier(2, 0, b, [x.base for x in new]))
+        for x in old:
+            x.close()
+        for t in range(15, 30):
+            got = run.step(ids[t])
+            keys = np.arange(m.layers)[:, None] * m.units + ids[t]
+            assert np.array_equal(got, want[keys]), "token %d read wrong bytes after the re-plan" % t
+            assert np.array_equal(run.ctx.table(run.keys), t_ref[t]), "slot table differs after token %d" % t
+        for L in range(m.layers):
+            for u in range(m.units):
+                run.ctx.check_unit(L, u)
+    finally:
+        run.close()
+        for x in old + new:
+            x.close()
+
+
 def _two_gpu_rank(rank, world, port, path, out_dir):
     import torch.distributed as dist
     os.environ["MASTER_ADDR"] = "127.0.0.1"
@@ -115,7 +159,13 @@ def _two_gpu_rank(rank, world, port, path, out_dir):
         setup = peer.PeerSetup(desc, route_counts(m, ids[:10]), dist, world, rank, rank, verify=True, copy=0,
                                collective_device=torch.device("cuda", rank))
         run = harness.DgRun(m, residents_per_layer=3, max_ids=2, peer=setup.tier)
-        got = np.stack([run.step(ids[t]) for t in range(ids.shape[0])])
+        got = [run.step(ids[t]) for t in range(15)]
+        # a planning round mid-decode: other counts, new owners, stores migrated over NVLink, the context switched
+        mig = setup.replan(desc, route_counts(m, synth.zipf_trace(10, m.layers, m.units, 2, s=1.0, seed=70 + rank)),
+                           dist, world, rank, rank, ctx=run.ctx, collective_device=torch.device("cuda", rank))
+        assert mig["units"] == (setup.owner == rank).sum()
+        got += [run.step(ids[t]) for t in range(15, ids.shape[0])]
+        got = np.stack(got)
         tables = np.stack([run.ctx.table(run.keys)])  # final table only; per-token parity is checked below
         np.savez(os.path.join(out_dir, "r%d.npz" % rank), got=got, owner=setup.owner, table=tables[0],
                  resident=np.array(run.resident_keys))

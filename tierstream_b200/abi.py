@@ -214,6 +214,8 @@ _PROTOS = {
     "tsb_peer_map": (C.c_int, [vp, C.c_int, P(vp)]),
     "tsb_peer_unmap": (C.c_int, [vp]),
     "tsb_open_peer": (C.c_int, [vp, P(ss_budget), vp, P(ss_options), P(tsb_peer_tier), P(vp)]),
+    "tsb_peer_store_migrate": (C.c_int, [vp, P(C.c_int32), P(vp), u32, u32, vp, P(u64), P(u64), P(u64)]),
+    "tsb_dg_peer_retier": (C.c_int, [vp, P(tsb_peer_tier)]),
     "tsb_test_dg_replay": (C.c_int, [P(dg_replay_config), P(i32), P(i32), P(i32), P(u64), P(C.c_uint8), P(u64)]),
     "tsb_test_dg_table": (C.c_int, [vp, P(i32), u32]),
     "tsb_xxh64": (u64, [vp, C.c_size_t, u64]),

@@ -681,32 +681,64 @@ ss_status tsb_peer_unmap(void* base) {
   return guard([&] { tsb::ipc_unmap(base); });
 }
 
+namespace {
+// A tsb_peer_tier checked and turned into the library's form (keys: the gated units of the descriptor).
+tsb::PeerTier tier_from(const tsb_peer_tier* peer, uint32_t keys) {
+  tsb::PeerTier t;
+  need(peer->struct_size >= sizeof(tsb_peer_tier), "tsb_peer_tier: struct_size is smaller than this build's");
+  need(peer->world >= 1, "tsb_peer_tier: world must be >= 1");
+  need(peer->rank >= 0 && uint32_t(peer->rank) < peer->world, "tsb_peer_tier: rank outside [0, world)");
+  need(peer->copy <= 1, "tsb_peer_tier: copy must be 0 (land kernel) or 1 (copy engines)");
+  need(peer->owner && peer->store_base, "tsb_peer_tier: null owner or store_base");
+  tsb::require(peer->keys == keys, SS_E_INVALID,
+               "tsb_peer_tier: keys " + std::to_string(peer->keys) + " where the descriptor has " +
+                   std::to_string(keys) + " gated units");
+  t.world = peer->world;
+  t.rank = peer->rank;
+  t.copy = int(peer->copy);
+  t.owner.assign(peer->owner, peer->owner + peer->keys);
+  std::vector<uint64_t> per;
+  t.index = tsb::store_index(t.owner, t.world, &per);
+  for (uint32_t r = 0; r < peer->world; ++r) t.base.push_back(static_cast<char*>(peer->store_base[r]));
+  for (uint32_t r = 0; r < t.world; ++r)
+    tsb::require(!per[r] || t.base[r], SS_E_INVALID,
+                 "tsb_peer_tier: rank " + std::to_string(r) + " owns " + std::to_string(per[r]) +
+                     " units but its store_base is null");
+  t.all_owned = std::all_of(t.owner.begin(), t.owner.end(), [](int32_t o) { return o >= 0; });
+  return t;
+}
+}  // namespace
+
+ss_status tsb_dg_peer_retier(ss_ctx* c, const tsb_peer_tier* peer) {
+  return ctx_guard(c, [&] {
+    need(peer != nullptr, "tsb_dg_peer_retier: null tier");
+    auto& dg = dg_of(c, "tsb_dg_peer_retier");
+    dg.set_peer(tier_from(peer, peer->keys));
+  });
+}
+
+ss_status tsb_peer_store_migrate(tsb_peer_store* dst, const int32_t* old_owner, void* const* old_base, uint32_t keys,
+                                 uint32_t world, void* stream, uint64_t* moved_units, uint64_t* moved_peer_units,
+                                 uint64_t* moved_bytes) {
+  return guard([&] {
+    need(dst && dst->s && old_owner && old_base, "tsb_peer_store_migrate: null argument");
+    need(world >= 1, "tsb_peer_store_migrate: world must be >= 1");
+    std::vector<char*> bases;
+    for (uint32_t r = 0; r < world; ++r) bases.push_back(static_cast<char*>(old_base[r]));
+    const tsb::Migration m =
+        tsb::migrate_store(*dst->s, std::vector<int32_t>(old_owner, old_owner + keys), bases, stream);
+    if (moved_units) *moved_units = m.units;
+    if (moved_peer_units) *moved_peer_units = m.peer_units;
+    if (moved_bytes) *moved_bytes = m.bytes;
+  });
+}
+
 ss_status tsb_open_peer(const ss_desc* d, const ss_budget* budget, const ss_plan* plan, const ss_options* opt,
                         const tsb_peer_tier* peer, ss_ctx** out) {
   tsb::PeerTier t;
   const ss_status st = guard([&] {
     need(d && peer, "tsb_open_peer: null argument");
-    need(peer->struct_size >= sizeof(tsb_peer_tier), "tsb_peer_tier: struct_size is smaller than this build's");
-    need(peer->world >= 1, "tsb_peer_tier: world must be >= 1");
-    need(peer->rank >= 0 && uint32_t(peer->rank) < peer->world, "tsb_peer_tier: rank outside [0, world)");
-    need(peer->copy <= 1, "tsb_peer_tier: copy must be 0 (land kernel) or 1 (copy engines)");
-    need(peer->owner && peer->store_base, "tsb_peer_tier: null owner or store_base");
-    const tsb::GatedKeys gk = tsb::gated_keys(d->d);
-    tsb::require(peer->keys == gk.keys(), SS_E_INVALID,
-                 "tsb_peer_tier: keys " + std::to_string(peer->keys) + " where the descriptor has " +
-                     std::to_string(gk.keys()) + " gated units");
-    t.world = peer->world;
-    t.rank = peer->rank;
-    t.copy = int(peer->copy);
-    t.owner.assign(peer->owner, peer->owner + peer->keys);
-    std::vector<uint64_t> per;
-    t.index = tsb::store_index(t.owner, t.world, &per);
-    for (uint32_t r = 0; r < peer->world; ++r) t.base.push_back(static_cast<char*>(peer->store_base[r]));
-    for (uint32_t r = 0; r < t.world; ++r)
-      tsb::require(!per[r] || t.base[r], SS_E_INVALID,
-                   "tsb_peer_tier: rank " + std::to_string(r) + " owns " + std::to_string(per[r]) +
-                       " units but its store_base is null");
-    t.all_owned = std::all_of(t.owner.begin(), t.owner.end(), [](int32_t o) { return o >= 0; });
+    t = tier_from(peer, tsb::gated_keys(d->d).keys());
   });
   if (st != SS_OK) return st;
   return open_impl(d, budget, plan, opt, &t, out);

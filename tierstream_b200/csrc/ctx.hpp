@@ -26,6 +26,8 @@ class DeviceScope {
   int prev_ = -1;
 };
 
+struct PeerTier;
+
 class DgContext {
  public:
   virtual ~DgContext() = default;
@@ -58,6 +60,9 @@ class DgContext {
   virtual void exclusive_stats(ss_exclusive_stats* out) const = 0;
   virtual std::string stats_json() const = 0;
   virtual void reset_open() = 0;
+  // The peer tier's owners and store addresses replaced between tokens (a re-plan): the same ranks, the same set of
+  // owned keys; every copy that read the old stores has finished when it returns.
+  virtual void set_peer(const PeerTier& t) = 0;
   // test hooks (ss_test.h), refused unless opened with dg_test_hooks
   virtual void test_mutate(int m) = 0;
   virtual void test_pressure(uint32_t free_per_token, uint32_t evict_recent) = 0;

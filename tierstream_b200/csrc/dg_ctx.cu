@@ -922,6 +922,21 @@ class CudaDgContext final : public DgContext {
     }
     return uint32_t(keys.size());
   }
+  void set_peer(const PeerTier& t) override {
+    require(!in_token_, SS_E_INVALID, "tsb_dg_peer_retier: between tokens only");
+    require(peer_ != nullptr, SS_E_INVALID,
+            "tsb_dg_peer_retier: the context was opened without the peer tier (tsb_open_peer)");
+    require(t.world == peer_->world && t.rank == peer_->rank, SS_E_INVALID,
+            "tsb_dg_peer_retier: world and rank must stay those of the open");
+    require(t.owner.size() == peer_->owner.size(), SS_E_INVALID, "tsb_dg_peer_retier: the owner map covers other keys");
+    for (size_t k = 0; k < t.owner.size(); ++k)
+      require((t.owner[k] >= 0) == (peer_->owner[k] >= 0), SS_E_INVALID,
+              "tsb_dg_peer_retier: key " + std::to_string(k) + " would join or leave the tier (only owners change: a "
+              "unit's block holds no bytes while it is owned)");
+    core_->drain();
+    mover_->drain_all();  // no copy reads an old store after this
+    *peer_ = t;
+  }
   void set_sched(uint32_t wb_defer, uint32_t flush_ready) override {
     require(!in_token_, SS_E_INVALID, "ss_dg_set_sched: between tokens only");
     require(wb_defer <= 1 && flush_ready <= 1, SS_E_INVALID, "ss_dg_set_sched: 0 or 1 each");

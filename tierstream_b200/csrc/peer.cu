@@ -102,6 +102,9 @@ PeerStore::PeerStore(const Desc& d, const std::vector<int32_t>& owner, int32_t r
       if (owner[gk.base[g] + u] == rank) mine.push_back({g, u});
   units_ = mine.size();
   bytes_ = units_ * gk.unit_bytes;
+  unit_bytes_ = gk.unit_bytes;
+  rank_ = rank;
+  owner_ = owner;
   if (!bytes_) return;
   ck(cudaMalloc(reinterpret_cast<void**>(&base_), size_t(bytes_)), "cudaMalloc (peer store)");
   if (!fill) {
@@ -237,6 +240,51 @@ void* ipc_map(const void* handle, int device) {
 
 void ipc_unmap(void* base) {
   if (base) ck(cudaIpcCloseMemHandle(base), "cudaIpcCloseMemHandle (peer store)");
+}
+
+Migration migrate_store(PeerStore& dst, const std::vector<int32_t>& old_owner, const std::vector<char*>& old_base,
+                        void* stream) {
+  const auto t0 = std::chrono::steady_clock::now();
+  const std::vector<int32_t>& now = dst.owner();
+  require(old_owner.size() == now.size(), SS_E_INVALID,
+          "tsb_peer_store_migrate: the old owner map has " + std::to_string(old_owner.size()) + " keys, the store's " +
+              std::to_string(now.size()));
+  const uint32_t world = uint32_t(old_base.size());
+  std::vector<uint64_t> per;
+  const std::vector<int64_t> old_index = store_index(old_owner, world, &per);
+  Migration m;
+  const uint64_t ub = dst.unit_bytes();
+  DeviceScope on(dst.device());
+  auto b = std::make_unique<dev::Batch>();
+  uint64_t chunks = 0;
+  auto launch = [&] {
+    if (!b->n_copies) return;
+    const int grid = int(std::min<uint64_t>(std::max<uint64_t>(chunks, 1), 296));
+    ck(cudaError_t(dev::launch_batch(*b, grid, stream)), "land kernel (migration)");
+    b->n_copies = 0;
+    chunks = 0;
+  };
+  uint64_t i = 0;
+  for (size_t k = 0; k < now.size(); ++k) {
+    if (now[k] != dst.rank()) continue;
+    const int32_t o = old_owner[k];
+    require(o >= 0, SS_E_INVALID,
+            "tsb_peer_store_migrate: key " + std::to_string(k) + " joins the tier (unowned before): a new store reads "
+            "such units from their file (tsb_peer_store_create)");
+    require(uint32_t(o) < world && old_base[size_t(o)], SS_E_INVALID,
+            "tsb_peer_store_migrate: no store address for rank " + std::to_string(o));
+    if (b->n_copies == dev::kMaxCopies) launch();
+    b->copies[b->n_copies++] = {old_base[size_t(o)] + uint64_t(old_index[k]) * ub, dst.base() + i * ub, ub};
+    chunks += (ub + (64u << 10) - 1) >> 16;
+    ++m.units;
+    if (o != dst.rank()) ++m.peer_units;
+    ++i;
+  }
+  launch();
+  ck(cudaStreamSynchronize(static_cast<cudaStream_t>(stream)), "cudaStreamSynchronize (migration)");
+  m.bytes = m.units * ub;
+  m.seconds = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+  return m;
 }
 
 PeerStore::~PeerStore() {

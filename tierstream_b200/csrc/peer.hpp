@@ -68,13 +68,29 @@ class PeerStore {
   uint64_t bytes() const { return bytes_; }
   uint64_t units() const { return units_; }
   int device() const { return device_; }
+  uint64_t unit_bytes() const { return unit_bytes_; }
+  int32_t rank() const { return rank_; }
+  const std::vector<int32_t>& owner() const { return owner_; }
   double fill_seconds() const { return fill_s_; }
 
  private:
   char* base_ = nullptr;
-  uint64_t bytes_ = 0, units_ = 0;
+  uint64_t bytes_ = 0, units_ = 0, unit_bytes_ = 0;
   int device_ = 0;
+  int32_t rank_ = -1;
+  std::vector<int32_t> owner_;  // the owner map the store was made for
   double fill_s_ = 0;
 };
+
+// A re-plan's migration: fills `dst` (allocated for `new_owner`, this rank's units of it in key order) with every
+// unit from where it lives now, `old_owner` / `old_base` (each rank's current store as seen from this process: a
+// peer's over NVLink, this rank's own in HBM), by the land kernel on `stream`; returns after the copies landed. Every
+// unit of dst must be owned under old_owner (a unit joining the tier is read from its file by a new store instead).
+struct Migration {
+  uint64_t units = 0, peer_units = 0, bytes = 0;
+  double seconds = 0;
+};
+Migration migrate_store(PeerStore& dst, const std::vector<int32_t>& old_owner, const std::vector<char*>& old_base,
+                        void* stream);
 
 }  // namespace tsb

@@ -63,6 +63,17 @@ class Store:
         abi.check(abi.load().tsb_peer_store_export(self.h, buf))
         return bytes(buf)
 
+    def migrate_from(self, old_owner, old_bases, stream):
+        """Fills this store (allocated for its new owners) from where its units live now (tsb_peer_store_migrate):
+        (units, units from peers, bytes)."""
+        old_owner = np.ascontiguousarray(old_owner, dtype=np.int32)
+        bases = (C.c_void_p * len(old_bases))(*[b or None for b in old_bases])
+        u, pu, by = C.c_uint64(), C.c_uint64(), C.c_uint64()
+        abi.check(abi.load().tsb_peer_store_migrate(self.h, old_owner.ctypes.data_as(C.POINTER(C.c_int32)),
+                                                    C.cast(bases, C.POINTER(C.c_void_p)), old_owner.size,
+                                                    len(old_bases), stream, C.byref(u), C.byref(pu), C.byref(by)))
+        return u.value, pu.value, by.value
+
     def close(self):
         if getattr(self, "h", None):
             abi.load().tsb_peer_store_free(self.h)
@@ -165,6 +176,43 @@ class PeerSetup:
         self.tier = Tier(world, rank, self.owner, bases, copy)
         if dist is not None:
             dist.barrier()
+
+    def replan(self, desc, local_counts, dist, world, rank, device, ctx=None, cap_units=None, collective_device=None):
+        """A planning round: the ranks' fresh routing counts summed (one all-reduce), the owners planned again, every
+        rank's new store filled from the current stores (peers over NVLink, its own in HBM), the new stores'
+        handles exchanged, and `ctx` (if given) switched to the new tier between tokens; the old stores are released
+        once every rank switched. Returns {units, peer_units, bytes, seconds} of this rank's migration."""
+        import time
+
+        import torch
+        counts = local_counts if dist is None else all_reduce_counts(local_counts, dist, collective_device)
+        new_owner = plan_owners(counts, world, cap_units)
+        old_owner, old_bases = self.owner, [self.tier.bases[r] for r in range(world)]
+        store = Store(desc, new_owner, rank, device, verify=False, fill=False)
+        s = torch.cuda.Stream(device=device)
+        t0 = time.perf_counter()
+        units, peer_units, nbytes = store.migrate_from(old_owner, old_bases, s.cuda_stream)
+        seconds = time.perf_counter() - t0
+        if dist is not None:
+            dist.barrier()  # every rank is done reading the old stores
+        handles = ([store.handle()] if dist is None else
+                   all_gather_handles(store.handle(), dist, world, collective_device))
+        mapped, bases = [], []
+        for r in range(world):
+            if r == rank:
+                bases.append(store.base)
+            else:
+                b = map_store(handles[r], device)
+                mapped.append(b)
+                bases.append(b)
+        tier = Tier(world, rank, new_owner, bases, self.tier.copy)
+        if ctx is not None:
+            ctx.retier(tier)
+        if dist is not None:
+            dist.barrier()  # every context reads the new stores only
+        self.close()
+        self.store, self.mapped, self.tier, self.owner, self.counts = store, mapped, tier, new_owner, counts
+        return {"units": units, "peer_units": peer_units, "bytes": nbytes, "seconds": seconds}
 
     def close(self):
         for b in getattr(self, "mapped", []):

@@ -1,4 +1,5 @@
-"""NVLink pull rate of the peer tier's mover (K5), one process per GPU under torchrun:
+"""NVLink pull rate of the peer tier's mover (K5), and a planning round's store migration, one process per GPU under
+torchrun:
 
     python -m torch.distributed.run --nproc-per-node N --master-addr 127.0.0.1 -m tierstream_b200.peer_bench
 
@@ -6,8 +7,10 @@ Every rank fills its store (the units it owns of the benchmark's Mixtral-shaped 
 summed routing counts), the ranks exchange the stores' IPC handles, then rank r copies `--units` units of rank
 (r + 1) % N's store into a local buffer, every rank at once (each GPU's link carries one pull in and one out), with
 (a) one land-kernel launch (SM loads over NVLink) and (b) the copy engines (cudaMemcpyAsync per part), each timed
-with CUDA events on the launching stream after warm-up; then rank 0 alone. Rank 0 prints one JSON line with the
-per-rank GB/s (max-time over ranks) against the pool's measured 770 GB/s per direction.
+with CUDA events on the launching stream after warm-up; then rank 0 alone. Then a re-plan from other routing counts
+migrates every rank's store (new stores filled from the current ones: peers over NVLink, its own in HBM), timed on
+the host around the copies, max over ranks. Rank 0 prints one JSON line with the per-rank GB/s (max-time over ranks)
+against the pool's measured 770 GB/s per direction, and the migration's aggregate GB/s.
 """
 import argparse
 import ctypes as C
@@ -113,6 +116,22 @@ def main():
         for row, k in zip(got, own_keys[[0, n - 1]]):
             want = model.unit_bytes_of(int(k) // UNITS, int(k) % UNITS)
             assert np.array_equal(row, want), "rank %d pulled wrong bytes of key %d" % (rank, k)
+        # a planning round: other routing counts, new owners, every rank's new store filled from the current ones
+        cal2 = synth.zipf_trace(64, LAYERS, UNITS, 2, s=1.1, seed=5001 + rank)
+        counts2 = np.bincount((np.arange(LAYERS)[None, :, None] * UNITS + cal2).reshape(-1),
+                              minlength=LAYERS * UNITS)
+        dist.barrier()
+        mig = setup.replan(runtime.Desc(model.desc()), counts2, dist, world, rank, local, collective_device=dev)
+        t = torch.tensor([mig["seconds"], float(mig["bytes"]), float(mig["peer_units"] * unit)], dtype=torch.float64,
+                         device=dev)
+        tmax = t[:1].clone()
+        dist.all_reduce(tmax, op=dist.ReduceOp.MAX)
+        tsum = t[1:].clone()
+        dist.all_reduce(tsum, op=dist.ReduceOp.SUM)
+        out["replan_migration"] = {"seconds_max_over_ranks": round(float(tmax.item()), 4),
+                                   "bytes_all_ranks": int(tsum[0].item()),
+                                   "bytes_from_peers_all_ranks": int(tsum[1].item()),
+                                   "gbs_all_ranks": round(float(tsum[0].item()) / float(tmax.item()) / 1e9, 2)}
         if rank == 0:
             print(json.dumps({"bench": "peer pull (K5)", "n_gpus": world, "units_per_rank": n, "unit_bytes": unit,
                               "bytes_per_rank": moved, "peak_gbs_per_direction": 770.0,

@@ -131,6 +131,12 @@ class DgContext:
     def reset_open(self):
         abi.check(abi.load().ss_dg_reset_open(self.h))
 
+    def retier(self, tier):
+        """Between tokens: the peer tier's owners and store addresses replaced (tsb_dg_peer_retier)."""
+        t = tier.struct()
+        abi.check(abi.load().tsb_dg_peer_retier(self.h, C.byref(t)))
+        self.peer = tier
+
     def timeline(self, g):
         """The last token's timeline of gated layer g (ss_dg_timeline; -1 where not measured)."""
         t = abi.ss_dg_layer_timeline()
