@@ -121,3 +121,13 @@ def test_open_peer_refuses_bad_tiers():
     assert b"store_base is null" in lib.ss_last_error()
     t = peer.Tier(1, 0, owner, [0x1000], copy=2)
     assert opened(t) == abi.SS_E_INVALID
+
+
+def test_replan_entry_points_refuse_bad_arguments():
+    lib = abi.load()
+    t = peer.Tier(1, 0, np.zeros(4, dtype=np.int32), [0x1000]).struct()
+    assert lib.tsb_dg_peer_retier(None, C.byref(t)) == abi.SS_E_INVALID
+    owner = (C.c_int32 * 4)()
+    bases = (C.c_void_p * 1)()
+    assert lib.tsb_peer_store_migrate(None, owner, bases, 4, 1, None, None, None, None) == abi.SS_E_INVALID
+    assert b"null argument" in lib.ss_last_error()

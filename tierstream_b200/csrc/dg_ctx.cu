@@ -933,8 +933,9 @@ class CudaDgContext final : public DgContext {
       require((t.owner[k] >= 0) == (peer_->owner[k] >= 0), SS_E_INVALID,
               "tsb_dg_peer_retier: key " + std::to_string(k) + " would join or leave the tier (only owners change: a "
               "unit's block holds no bytes while it is owned)");
-    core_->drain();
-    mover_->drain_all();  // no copy reads an old store after this
+    // every copy issued so far has landed (the streams synced; the cache's own state is left as it is, so its
+    // decisions stay those of an uninterrupted run): no copy reads an old store after this
+    for (Mover::Stream st : {Mover::kDem, Mover::kPf, Mover::kD2h}) mover_->sync(st);
     *peer_ = t;
   }
   void set_sched(uint32_t wb_defer, uint32_t flush_ready) override {
