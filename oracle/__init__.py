@@ -50,7 +50,7 @@ def ref():
         lib.oref_host_replay.restype = C.c_int
         lib.oref_host_replay.argtypes = [C.c_char_p, C.c_size_t, C.c_void_p, C.c_size_t, C.c_void_p, C.c_void_p,
                                          C.c_uint32, C.c_void_p, C.c_uint32, C.c_void_p, C.c_void_p, C.c_void_p,
-                                         C.c_void_p, C.c_char_p, C.c_size_t]
+                                         C.c_void_p, C.c_void_p, C.c_uint32, C.c_int, C.c_char_p, C.c_size_t]
         lib.oref_dg_replay.restype = C.c_int
         lib.oref_dg_replay.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
                                        C.c_void_p, C.c_char_p, C.c_size_t]
@@ -58,10 +58,14 @@ def ref():
     return _ref
 
 
-def ref_host_replay(desc_json, tiers, budget, options, routes, all_layers, want_exclusive=False):
+def ref_host_replay(desc_json, tiers, budget, options, routes, all_layers, want_exclusive=False, pf_ids=None,
+                    pf_mode=0):
     """The reference's host forward mode (CPU backend) over routes [forwards][layers][n_ids]: (locs [forwards][units][2],
-    stats [forwards][layers][5] = routed, hits, admitted, transient, evicted[, exclusive [forwards][8] = writebacks,
-    writeback_bytes, deferred, promoted, free_blocks, min_free_blocks, rereads, discards after each forward])."""
+    stats [forwards][layers][9] = routed, hits, admitted, transient, evicted, prefetched, spec_issued, spec_used,
+    spec_dropped[, exclusive [forwards][8] = writebacks,
+    writeback_bytes, deferred, promoted, free_blocks, min_free_blocks, rereads, discards after each forward]).
+    Prefetches (pf_mode 1 certain pf_ids, 2 speculative pf_ids [forwards][layers][n], 3 whole layers): layer 0's
+    before ss_begin, layer L + 1's before the routes of layer L."""
     import numpy as np
     routes = np.ascontiguousarray(routes, dtype=np.int32)
     F, L, n = routes.shape
@@ -69,13 +73,16 @@ def ref_host_replay(desc_json, tiers, budget, options, routes, all_layers, want_
     t = np.ascontiguousarray(tiers, dtype=np.uint8)
     al = np.ascontiguousarray(all_layers, dtype=np.uint8)
     locs = np.empty((F, total, 2), dtype=np.int32)
-    stats = np.empty((F, L, 5), dtype=np.uint64)
+    stats = np.empty((F, L, 9), dtype=np.uint64)
     err = C.create_string_buffer(512)
     raw = desc_json.encode()
     xs = np.zeros((F, 8), dtype=np.uint64) if want_exclusive else None
+    pf = np.ascontiguousarray(pf_ids, dtype=np.int32) if pf_ids is not None else None
+    n_pf = pf.shape[2] if pf is not None else 0
     rc = ref().oref_host_replay(raw, len(raw), t.ctypes.data, t.size, C.byref(budget), C.byref(options), F,
                                 routes.ctypes.data, n, al.ctypes.data, locs.ctypes.data, stats.ctypes.data,
-                                xs.ctypes.data if xs is not None else None, err, 512)
+                                xs.ctypes.data if xs is not None else None, pf.ctypes.data if pf is not None else None,
+                                n_pf, pf_mode, err, 512)
     if rc != 0:
         raise RuntimeError("reference host replay failed: " + err.value.decode())
     return (locs, stats, xs) if want_exclusive else (locs, stats)

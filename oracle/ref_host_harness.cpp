@@ -37,7 +37,8 @@ struct ss_ctx {
 extern "C" __attribute__((visibility("default"))) int oref_host_replay(
     const char* desc_json, size_t len, const uint8_t* tiers, size_t n_tiers, const ss_budget* budget,
     const ss_options* opt_in, uint32_t forwards, const int32_t* routes, uint32_t n_ids, const uint8_t* all_layers,
-    int32_t* locs, uint64_t* stats, uint64_t* xstats, char* err, size_t errlen) {
+    int32_t* locs, uint64_t* stats, uint64_t* xstats, const int32_t* pf_ids, uint32_t n_pf, int pf_mode, char* err,
+    size_t errlen) {
   ss_desc* d = nullptr;
   ss_plan* p = nullptr;
   ss_ctx* c = nullptr;
@@ -60,12 +61,22 @@ extern "C" __attribute__((visibility("default"))) int oref_host_replay(
   std::vector<ss_layer_stats> before(static_cast<size_t>(L_n)), after(static_cast<size_t>(L_n));
   for (uint32_t f = 0; f < forwards; ++f) {
     for (int L = 0; L < L_n; ++L) ss_stats_layer(c, L, &before[size_t(L)]);
+    // prefetch schedule (pf_mode 1 certain ids, 2 speculative ids, 3 whole layer): layer 0 before ss_begin, layer
+    // L + 1 before the routes of layer L
+    auto prefetch = [&](int L) -> bool {
+      if (!pf_mode || L >= L_n || ss_desc_layer_units(d, L) <= 0) return true;
+      if (pf_mode == 3) return ss_prefetch_layer(c, L) == SS_OK;
+      const int32_t* p = pf_ids + (size_t(f) * size_t(L_n) + size_t(L)) * n_pf;
+      return ss_prefetch(c, L, p, int(n_pf), pf_mode == 2 ? SS_PREFETCH_SPECULATIVE : SS_PREFETCH_CERTAIN) == SS_OK;
+    };
+    if (!prefetch(0)) return bad("ss_prefetch");
     if (ss_begin(c, nullptr, 0) != SS_OK) return bad("ss_begin");
     int32_t* out = locs + size_t(f) * size_t(total) * 2;
     for (int64_t k = 0; k < total * 2; ++k) out[k] = k % 2 ? -1 : 0;
     for (int L = 0; L < L_n; ++L) {
       const int units = ss_desc_layer_units(d, L);
       if (units <= 0) continue;
+      if (!prefetch(L + 1)) return bad("ss_prefetch");
       const int32_t* r = routes + (size_t(f) * size_t(L_n) + size_t(L)) * n_ids;
       const ss_status st = all_layers[L] ? ss_layer_all(c, L) : ss_layer_routes(c, L, r, int(n_ids));
       if (st != SS_OK) return bad("routes");
@@ -84,12 +95,16 @@ extern "C" __attribute__((visibility("default"))) int oref_host_replay(
     if (ss_end(c) != SS_OK) return bad("ss_end");
     for (int L = 0; L < L_n; ++L) {
       ss_stats_layer(c, L, &after[size_t(L)]);
-      uint64_t* o5 = stats + (size_t(f) * size_t(L_n) + size_t(L)) * 5;
+      uint64_t* o5 = stats + (size_t(f) * size_t(L_n) + size_t(L)) * 9;
       o5[0] = after[size_t(L)].routed - before[size_t(L)].routed;
       o5[1] = after[size_t(L)].hits - before[size_t(L)].hits;
       o5[2] = after[size_t(L)].admitted - before[size_t(L)].admitted;
       o5[3] = after[size_t(L)].transient - before[size_t(L)].transient;
       o5[4] = after[size_t(L)].evicted - before[size_t(L)].evicted;
+      o5[5] = after[size_t(L)].prefetched - before[size_t(L)].prefetched;
+      o5[6] = after[size_t(L)].spec_issued - before[size_t(L)].spec_issued;
+      o5[7] = after[size_t(L)].spec_used - before[size_t(L)].spec_used;
+      o5[8] = after[size_t(L)].spec_dropped - before[size_t(L)].spec_dropped;
     }
     if (xstats) {  // the exclusive counters after the forward (cumulative): writebacks .. discards
       ss_exclusive_stats x;

@@ -90,7 +90,7 @@ def test_c1_tables_counters_and_bytes_match_reference(c1_model, orc, ref, dynami
             for L in range(m.layers):
                 a = ctx.layer_stats(L)
                 mine = [a[k] - before[L][k] for k in ("routed", "hits", "admitted", "transient", "evicted")]
-                assert mine == [int(x) for x in ref_stats[f, L]], "forward %d layer %d counters" % (f, L)
+                assert mine == [int(x) for x in ref_stats[f, L, :5]], "forward %d layer %d counters" % (f, L)
     finally:
         ctx.close()
 
@@ -205,7 +205,110 @@ def test_c1_exclusive_mode_matches_reference(c1_model, orc, ref, dynamic, spare_
             for L in range(m.layers):
                 a = ctx.layer_stats(L)
                 mine = [a[k] - before[L][k] for k in ("routed", "hits", "admitted", "transient", "evicted")]
-                assert mine == [int(x) for x in ref_stats[f, L]], "forward %d layer %d counters" % (f, L)
+                assert mine == [int(x) for x in ref_stats[f, L, :5]], "forward %d layer %d counters" % (f, L)
             assert ctx.exclusive_stats() == [int(x) for x in ref_x[f]], "forward %d exclusive counters" % f
+    finally:
+        ctx.close()
+
+
+def run_with_prefetch(m, ctx, routes, pf, mode, ref_locs, ref_stats, want, all_layers=False):
+    """Drives forwards the way the reference harness does (layer 0's prefetch before ss_begin, layer L + 1's before
+    the routes of layer L) and checks tables, the nine counters and the bytes read through the table."""
+    eng = abi.load_engine()
+    s = torch.cuda.Stream()
+    ids_dev = torch.zeros(m.units, dtype=torch.int32, device="cuda")
+    out = torch.zeros(m.units, dtype=torch.int64, device="cuda")
+    keys9 = ("routed", "hits", "admitted", "transient", "evicted", "prefetched", "spec_issued", "spec_used",
+             "spec_dropped")
+
+    def prefetch(f, L):
+        if L >= m.layers:
+            return
+        if mode == 3:
+            ctx.prefetch_layer(L)
+        else:
+            ctx.prefetch(L, pf[f, L], speculative=mode == 2)
+
+    for f in range(routes.shape[0]):
+        before = [ctx.layer_stats(L) for L in range(m.layers)]
+        prefetch(f, 0)
+        ctx.begin()
+        for L in range(m.layers):
+            prefetch(f, L + 1)
+            if all_layers:
+                ctx.layer_all(L)
+                ids = np.arange(m.units, dtype=np.int32)
+            else:
+                ctx.routes(L, routes[f, L])
+                ids = np.unique(routes[f, L]).astype(np.int32)
+            v = ctx.acquire(L, s.cuda_stream)
+            assert np.array_equal(ctx.locs(L, m.units), ref_locs[f, L * m.units:(L + 1) * m.units]), \
+                "forward %d layer %d: table differs from the reference" % (f, L)
+            with torch.cuda.stream(s):
+                ids_dev[:ids.size].copy_(torch.from_numpy(ids), non_blocking=False)
+                assert eng.tse_read_table(C_ptr(v.table_dev), ids_dev.data_ptr(), ids.size, m.unit_bytes,
+                                          out.data_ptr(), 16, s.cuda_stream) == 0
+            s.synchronize()
+            got = out[:ids.size].cpu().numpy().astype(np.uint64)
+            assert np.array_equal(got, want[L * m.units + ids]), "forward %d layer %d: wrong bytes" % (f, L)
+            ctx.release(L, s.cuda_stream)
+        ctx.end()
+        for L in range(m.layers):
+            a = ctx.layer_stats(L)
+            mine = [a[k] - before[L][k] for k in keys9]
+            assert mine == [int(x) for x in ref_stats[f, L]], "forward %d layer %d counters %s vs %s" % (
+                f, L, mine, ref_stats[f, L].tolist())
+
+
+@pytest.mark.parametrize("mode,dynamic", [(2, 2), (2, 0), (1, 2), (1, 0)])
+def test_c1_prefetch_matches_reference(c1_model, orc, ref, mode, dynamic):
+    """ss_prefetch ahead of the routes (speculative guesses through the stream ring within lookahead_budget, or
+    certain ids admitted as demands), layer 0's issued between forwards: tables, the nine counters (prefetched and
+    the speculative issued / used / dropped among them) and the bytes equal the reference's."""
+    m = c1_model
+    tiers, b, o = setup(m, dynamic=dynamic, pin_planned=0)
+    routes = synth.zipf_trace(24, m.layers, m.units, 2, seed=1, uniform=True)
+    pf = synth.zipf_trace(24, m.layers, m.units, 3, seed=9, uniform=True) if mode == 2 else routes
+    desc_json = m.desc(order="ranked")
+    ref_locs, ref_stats = oracle.ref_host_replay(desc_json, tiers, b, o, routes, [0] * m.layers, pf_ids=pf,
+                                                 pf_mode=mode)
+    assert ref_stats[:, :, 5:].sum() > 0, "the schedule must prefetch"
+    desc = runtime.Desc(desc_json)
+    plan = runtime.Plan(desc, b, tiers=tiers)
+    ctx = runtime.HostContext(desc, plan, o)
+    try:
+        run_with_prefetch(m, ctx, routes, pf, mode, ref_locs, ref_stats, expected(m, orc))
+    finally:
+        ctx.close()
+
+
+def test_layer_prefetch_overlaps_the_blob_stream(orc, ref):
+    """C3-shaped, scaled: ss_prefetch_layer(L + 1) before layer L's ss_layer_all, through a 2-slot ring."""
+    m = synth.Model(os.path.join(harness.model_dir(), "tsb-test-blobs.bin"), layers=12, units=1,
+                    part_bytes=((1 << 20) + 17,), seed=5, top_k=1)
+    m.write()
+    import json
+    d = json.loads(m.desc(order="prefix"))
+    for lay in d["layers"]:
+        lay["kind"] = "blob"
+        lay.pop("top_k")
+    desc_json = json.dumps(d)
+    tiers = [abi.SS_TIER_RESIDENT] * 5 + [abi.SS_TIER_PINNED] * 7
+    b = abi.budget_defaults()
+    b.device_bytes = 1 << 30
+    b.margin_gib = 1.0 / 1024
+    b.margin_fraction = 0.0
+    b.ring_slots = 2
+    b.host_pinned_bytes = 1 << 30
+    o = abi.options_defaults()
+    o.forward_mode = abi.SS_FORWARD_HOST
+    routes = np.zeros((3, m.layers, 1), dtype=np.int32)
+    ref_locs, ref_stats = oracle.ref_host_replay(desc_json, tiers, b, o, routes, [1] * m.layers, pf_mode=3)
+    assert ref_stats[:, :, 5].sum() > 0
+    desc = runtime.Desc(desc_json)
+    plan = runtime.Plan(desc, b, tiers=tiers)
+    ctx = runtime.HostContext(desc, plan, o)
+    try:
+        run_with_prefetch(m, ctx, routes, None, 3, ref_locs, ref_stats, expected(m, orc), all_layers=True)
     finally:
         ctx.close()

@@ -169,6 +169,10 @@ _PROTOS = {
     "ss_end": (C.c_int, [vp]),
     "ss_layer_routes": (C.c_int, [vp, C.c_int, P(i32), C.c_int]),
     "ss_layer_all": (C.c_int, [vp, C.c_int]),
+    "ss_prefetch": (C.c_int, [vp, C.c_int, P(C.c_int32), C.c_int, C.c_int]),
+    "ss_prefetch_layer": (C.c_int, [vp, C.c_int]),
+    "ss_host_prefetch": (C.c_int, [vp, C.c_int, P(C.c_int32), C.c_int]),
+    "ss_host_prefetch_layer": (C.c_int, [vp, C.c_int]),
     "ss_acquire": (C.c_int, [vp, C.c_int, vp, P(ss_layer_view)]),
     "ss_acquire_groups": (C.c_int, [vp, C.c_int, vp, P(ss_layer_view)]),
     "ss_group_wait": (C.c_int, [vp, C.c_int, C.c_int, vp]),

@@ -380,10 +380,30 @@ ss_status ss_layer_routes_dev(ss_ctx* c, int layer, const int32_t* ids_dev, int 
 ss_status ss_layer_all(ss_ctx* c, int layer) {
   return ctx_guard(c, [&] { host_of(c, "ss_layer_all").routes_all(layer); });
 }
-ss_status ss_prefetch(ss_ctx*, int, const int32_t*, int, ss_prefetch_kind) { return unsupported("ss_prefetch"); }
-ss_status ss_prefetch_layer(ss_ctx*, int) { return unsupported("ss_prefetch_layer"); }
-ss_status ss_host_prefetch(ss_ctx*, int, const int32_t*, int) { return unsupported("ss_host_prefetch"); }
-ss_status ss_host_prefetch_layer(ss_ctx*, int) { return unsupported("ss_host_prefetch_layer"); }
+ss_status ss_prefetch(ss_ctx* c, int layer, const int32_t* ids, int n, ss_prefetch_kind kind) {
+  return ctx_guard(c, [&] {
+    need(n >= 0 && (ids || n == 0), "ss_prefetch: bad ids");
+    need(kind == SS_PREFETCH_CERTAIN || kind == SS_PREFETCH_SPECULATIVE, "ss_prefetch: unknown kind");
+    host_of(c, "ss_prefetch").prefetch(layer, ids, n, kind == SS_PREFETCH_SPECULATIVE);
+  });
+}
+ss_status ss_prefetch_layer(ss_ctx* c, int layer) {
+  return ctx_guard(c, [&] {
+    tsb::HostContext& h = host_of(c, "ss_prefetch_layer");
+    h.prefetch(layer, nullptr, -1, false);  // n < 0: every unit of the layer
+  });
+}
+// Host read-ahead buffers are not in this build (readahead_units must be 0 at open), where the reference's
+// ss_host_prefetch is a no-op too (stream_ctx.cpp:1442).
+ss_status ss_host_prefetch(ss_ctx* c, int, const int32_t* ids, int n) {
+  return ctx_guard(c, [&] {
+    need(n >= 0 && (ids || n == 0), "ss_host_prefetch: bad ids");
+    (void)host_of(c, "ss_host_prefetch");
+  });
+}
+ss_status ss_host_prefetch_layer(ss_ctx* c, int) {
+  return ctx_guard(c, [&] { (void)host_of(c, "ss_host_prefetch_layer"); });
+}
 ss_status ss_acquire(ss_ctx* c, int layer, void* s, ss_layer_view* out) {
   return ctx_guard(c, [&] {
     need(out != nullptr, "ss_acquire: null view");

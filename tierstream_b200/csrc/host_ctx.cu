@@ -54,7 +54,7 @@ uint64_t now_ns() {
 }
 
 struct Job {
-  enum State { Queued = 0, Done = 1, Failed = 2 };
+  enum State { Queued = 0, Done = 1, Failed = 2, Cancelled = 3 };  // Cancelled: a queued read dropped unread
   int layer = 0, unit = 0;
   char* dst = nullptr;             // device slot
   const char* pinned = nullptr;    // pinned tier source, null = its file
@@ -62,6 +62,7 @@ struct Job {
   cudaEvent_t src_wait_ev = nullptr;  // exclusive: the write-back into its block that has to land first
   cudaEvent_t dst_wb_ev = nullptr;    // exclusive: the write-back of the victim whose slot it lands in
   cudaEvent_t done_ev = nullptr;   // recorded on the copy stream after the copy
+  bool spec = false;               // a speculative prefetch's read, behind every demand read
   std::atomic<int> state{Queued};
   ss_status err_status = SS_OK;
   std::string err;
@@ -88,7 +89,7 @@ class HostCtx final : public HostContext {
 
   void seed(int layer, const int32_t* units, int n) override {
     check_layer(layer, "seed");
-    require(!in_fwd_, SS_E_INVALID, "seed: only between forwards");
+    require(!in_fwd_ && !fwd_open_, SS_E_INVALID, "seed: only between forwards");
     Lay& s = L_[size_t(layer)];
     require(s.rs != nullptr, SS_E_INVALID, "seed: layer has no units");
     require(n >= 0 && (units || n == 0), SS_E_INVALID, "seed: bad unit list");
@@ -126,24 +127,33 @@ class HostCtx final : public HostContext {
     if (st != SS_OK) fail(st, err);
   }
 
-  void begin(const uint32_t* rows, int n_layers) override {
-    require(!in_fwd_, SS_E_INVALID, "begin: previous forward not ended");
-    require(rows == nullptr || n_layers == int(L_.size()), SS_E_INVALID, "begin: rows_per_layer needs one per layer");
+  // The next forward's state, opened by ss_begin or by a prefetch between forwards (stream_ctx.cpp:1194-1213 there).
+  void open_forward() {
+    if (fwd_open_) return;
     for (size_t L = 0; L < L_.size(); ++L) {
       Lay& s = L_[L];
       std::fill(s.loc.begin(), s.loc.end(), int8_t(kNone));
       std::fill(s.slot.begin(), s.slot.end(), -1);
       std::fill(s.job.begin(), s.job.end(), nullptr);
       std::fill(s.count.begin(), s.count.end(), 0u);
+      std::fill(s.spec_unclaimed.begin(), s.spec_unclaimed.end(), char(0));
       s.routed.clear();
       s.pending.clear();
       s.hits.clear();
       s.groups.clear();
       s.gview.clear();
-      s.routes_given = s.acquired = s.released = false;
-      s.skip = rows ? rows[L] == 0 : false;
+      s.routes_given = s.acquired = s.released = s.skip = false;
     }
     std::fill(fwd_.begin(), fwd_.end(), ss_layer_stats{});
+    fwd_open_ = true;
+  }
+
+  void begin(const uint32_t* rows, int n_layers) override {
+    require(!in_fwd_, SS_E_INVALID, "begin: previous forward not ended");
+    require(rows == nullptr || n_layers == int(L_.size()), SS_E_INVALID, "begin: rows_per_layer needs one per layer");
+    open_forward();
+    if (rows)
+      for (size_t L = 0; L < L_.size(); ++L) L_[L].skip = rows[L] == 0;
     if (excl_) {
       xst_.free_blocks = free_block_count();
       xst_.min_free_blocks = std::min(xst_.min_free_blocks, xst_.free_blocks);
@@ -180,6 +190,52 @@ class HostCtx final : public HostContext {
     std::vector<int32_t> ids(static_cast<size_t>(n), 0);
     for (int u = 0; u < n; ++u) ids[size_t(u)] = u;
     ingest(layer, ids.data(), n);
+  }
+
+  // stream_ctx.cpp:1401-1440 there: certain prefetches are admitted as demands (ring when no slot), speculative ones
+  // take the stream ring only, at most lookahead_budget per call, and stop at a full ring; a later route claims them.
+  void prefetch(int layer, const int32_t* ids, int n, bool speculative) override {
+    check_layer(layer, "prefetch");
+    const Layer& l = d_.layers[size_t(layer)];
+    std::vector<int32_t> all;
+    if (n < 0) {  // the whole layer (ss_prefetch_layer)
+      for (int u = 0; u < l.n_units; ++u) all.push_back(u);
+      ids = all.data();
+      n = int(all.size());
+    }
+    open_forward();  // allowed between forwards: the copies belong to the next forward
+    Lay& s = L_[size_t(layer)];
+    require(s.rs != nullptr, SS_E_INVALID, "prefetch: layer has no units");
+    if (s.routes_given || s.acquired) return;  // too late to help
+    ss_layer_stats& st = fwd_[size_t(layer)];
+    uint32_t issued = 0;
+    std::vector<char> busy(size_t(l.n_units), 0);
+    for (int u = 0; u < l.n_units; ++u) busy[size_t(u)] = s.loc[size_t(u)] != kNone;
+    for (int i = 0; i < n; ++i) {
+      if (speculative && issued >= o_.lookahead_budget) break;
+      const int32_t u = ids[i];
+      if (u < 0 || u >= l.n_units) continue;
+      if (s.loc[size_t(u)] != kNone || s.rs->slot(u) >= 0) continue;
+      if (plan_.tier[size_t(gidx(layer, u))] == SS_TIER_PAIR) continue;
+      // a speculative read never evicts a resident on a guess: the ring only
+      const Admission a = speculative ? Admission{} : s.rs->admit({u}, busy, true, eviction_cap(layer));
+      xst_.deferred += uint64_t(a.deferred);
+      if (!a.admitted.empty()) {
+        fetch_admitted(layer, a);
+        st.evicted += a.evicted.size();
+      } else if (!fetch_into_ring(layer, u, speculative)) {
+        if (speculative) break;  // ring full: speculation never waits
+        s.pending.push_back(u);
+        s.loc[size_t(u)] = kRing;  // placed when a ring slot frees
+      }
+      busy[size_t(u)] = 1;
+      if (speculative) {
+        s.spec_unclaimed[size_t(u)] = 1;
+        ++st.spec_issued;
+      }
+      ++issued;
+    }
+    flush_copies();
   }
 
   void acquire(int layer, void* stream, bool wait_all, ss_layer_view* out) override {
@@ -263,9 +319,14 @@ class HostCtx final : public HostContext {
     ck(cudaEventRecord(s.release_ev, es), "cudaEventRecord (release)");
     ck(cudaEventRecord(s.table_ev[s.version], es), "cudaEventRecord (table)");
     s.released = true;
+    for (int u = 0; u < d_.layers[size_t(layer)].n_units; ++u)
+      if (s.spec_unclaimed[size_t(u)]) {
+        s.spec_unclaimed[size_t(u)] = 0;
+        ++fwd_[size_t(layer)].spec_dropped;
+      }
     for (size_t i = 0; i < ring_.size(); ++i) {
       if (ring_[i].owner != layer) continue;
-      if (ring_[i].job) wait_quiet(*ring_[i].job);
+      if (ring_[i].job && !cancel(ring_[i].job)) wait_quiet(*ring_[i].job);  // a read not started is dropped
       ring_owner_ev_[i] = s.release_ev;
       ring_[i].owner = -1;
       ring_[i].job.reset();
@@ -282,6 +343,7 @@ class HostCtx final : public HostContext {
     ss_status failed = SS_OK;
     std::string err;
     for (const JobPtr& j : fwd_jobs_) {
+      if (j->spec && cancel(j)) continue;  // a speculative read that has not started is dropped
       wait_quiet(*j);
       if (j->state.load() == Job::Failed && failed == SS_OK) {
         failed = j->err_status;
@@ -293,6 +355,7 @@ class HostCtx final : public HostContext {
       if (!s.rs) continue;
       bool any = false;
       for (int u = 0; u < d_.layers[L].n_units; ++u) {
+        if (s.spec_unclaimed[size_t(u)]) ++fwd_[L].spec_dropped;  // a layer never released: its unused guesses
         if (s.loc[size_t(u)] != kPersistent || !s.job[size_t(u)]) continue;
         if (s.job[size_t(u)]->state.load() != Job::Done) s.rs->drop(u);  // a failed read is read again at next use
         else any = true;
@@ -344,6 +407,7 @@ class HostCtx final : public HostContext {
     }
     if (hook_) hook_(hook_user_, &tot, fwd_.data(), int(L_.size()));
     in_fwd_ = false;
+    fwd_open_ = false;
     ++forwards_;
     if (failed != SS_OK) fail(failed, err);
   }
@@ -450,6 +514,7 @@ class HostCtx final : public HostContext {
     std::vector<int32_t> slot;
     std::vector<JobPtr> job;
     std::vector<uint32_t> count;
+    std::vector<char> spec_unclaimed;  // speculative prefetches no route claimed yet
     std::vector<int32_t> routed, pending, hits;
     std::vector<std::vector<int32_t>> groups;
     std::vector<ss_group> gview;
@@ -505,11 +570,12 @@ class HostCtx final : public HostContext {
   void pool_ev(cudaEvent_t e) {
     if (e) ev_pool_.push_back(e);
   }
-  JobPtr make_job(int layer, int unit, char* dst) {
+  JobPtr make_job(int layer, int unit, char* dst, bool spec = false) {
     JobPtr j = std::make_shared<Job>();
     j->layer = layer;
     j->unit = unit;
     j->dst = dst;
+    j->spec = spec;
     j->wait_ev = L_[size_t(layer)].release_ev;
     j->pinned = pinned_of_[size_t(gidx(layer, unit))];
     if (excl_ && j->pinned) {
@@ -528,9 +594,34 @@ class HostCtx final : public HostContext {
     }
     {
       std::lock_guard<std::mutex> lk(q_mu_);
-      queue_.push_back(j);
+      (j->spec ? spec_queue_ : queue_).push_back(j);
     }
     q_cv_.notify_one();
+  }
+  // A speculative read that is now a demand goes to the front of the demand queue if it has not started.
+  void promote(const JobPtr& j) {
+    std::lock_guard<std::mutex> lk(q_mu_);
+    if (!j->spec) return;
+    auto it = std::find(spec_queue_.begin(), spec_queue_.end(), j);
+    j->spec = false;
+    if (it == spec_queue_.end()) return;  // started (or a pinned copy, issued at once)
+    spec_queue_.erase(it);
+    queue_.push_front(j);
+  }
+  // A queued (not started) read is dropped: true; false when it started, so the caller waits for it.
+  bool cancel(const JobPtr& j) {
+    {
+      std::lock_guard<std::mutex> lk(q_mu_);
+      for (auto* q : {&queue_, &spec_queue_}) {
+        auto it = std::find(q->begin(), q->end(), j);
+        if (it == q->end()) continue;
+        q->erase(it);
+        j->state.store(Job::Cancelled);
+        done_cv_.notify_all();
+        return true;
+      }
+    }
+    return j->state.load() == Job::Cancelled;
   }
   void flush_copies() {
     if (batch_.empty()) return;
@@ -587,10 +678,11 @@ class HostCtx final : public HostContext {
       JobPtr j;
       {
         std::unique_lock<std::mutex> lk(q_mu_);
-        q_cv_.wait(lk, [&] { return stop_ || !queue_.empty(); });
-        if (stop_ && queue_.empty()) return;
-        j = queue_.front();
-        queue_.pop_front();
+        q_cv_.wait(lk, [&] { return stop_ || !queue_.empty() || !spec_queue_.empty(); });
+        if (stop_ && queue_.empty() && spec_queue_.empty()) return;
+        std::deque<JobPtr>& q = queue_.empty() ? spec_queue_ : queue_;  // speculative reads only when no demand waits
+        j = q.front();
+        q.pop_front();
       }
       size_t buf = 0;
       {
@@ -649,7 +741,7 @@ class HostCtx final : public HostContext {
     ck(cudaStreamWaitEvent(es, j.done_ev, 0), "cudaStreamWaitEvent (unit)");
   }
 
-  bool fetch_into_ring(int layer, int unit) {
+  bool fetch_into_ring(int layer, int unit, bool spec = false) {
     const uint64_t st = stride(layer);
     auto rc = std::find_if(rings_.begin(), rings_.end(), [&](const RingClass& r) { return r.stride == st; });
     if (rc == rings_.end()) return false;
@@ -658,7 +750,7 @@ class HostCtx final : public HostContext {
       if (ring_[i].owner >= 0) continue;
       rc->cursor = (i - rc->first + 1) % rc->count;
       Lay& s = L_[size_t(layer)];
-      JobPtr j = make_job(layer, unit, ring_[i].dev);
+      JobPtr j = make_job(layer, unit, ring_[i].dev, spec);
       fwd_jobs_.push_back(j);
       j->wait_ev = ring_owner_ev_[i];
       ring_[i].owner = layer;
@@ -781,6 +873,19 @@ class HostCtx final : public HostContext {
       if (!s.pending.empty()) return;  // layer order: a later layer never overtakes an earlier one
     }
   }
+  // The admitted units' copies into their slots; exclusive: the victims go back to free blocks first, and only a copy
+  // into a written-back victim's slot waits for that write-back.
+  void fetch_admitted(int layer, const Admission& a) {
+    size_t n_wb = 0;
+    cudaEvent_t wb_ev = excl_ && !a.evicted.empty() ? write_back(layer, a, &n_wb) : nullptr;
+    for (size_t k = 0; k < a.admitted.size(); ++k) {
+      cudaEvent_t wait = nullptr;
+      for (size_t i = 0; wb_ev && i < n_wb && !wait; ++i)
+        if (a.evicted_slot[i] == a.slot_of[k]) wait = wb_ev;
+      fetch_into_persistent(layer, a.admitted[k], a.slot_of[k], wait);
+    }
+  }
+
   void ingest(int layer, const int32_t* ids, int n) {
     Lay& s = L_[size_t(layer)];
     const Layer& l = d_.layers[size_t(layer)];
@@ -800,23 +905,24 @@ class HostCtx final : public HostContext {
       if (!s.count[size_t(u)] || plan_.tier[size_t(gidx(layer, u))] == SS_TIER_PAIR) continue;
       busy[size_t(u)] = 1;
       s.routed.push_back(u);
-      if (s.loc[size_t(u)] != kNone) ++st.prefetched;
-      else if (s.rs->slot(u) >= 0) s.hits.push_back(u);
+      if (s.loc[size_t(u)] != kNone) {  // prefetched this forward
+        if (s.spec_unclaimed[size_t(u)]) {
+          s.spec_unclaimed[size_t(u)] = 0;
+          ++st.spec_used;
+          if (s.job[size_t(u)]) promote(s.job[size_t(u)]);
+        } else {
+          ++st.prefetched;
+        }
+      } else if (s.rs->slot(u) >= 0) {
+        s.hits.push_back(u);
+      }
       else to_admit.push_back(u);
     }
     st.routed += s.routed.size();
     st.hits += s.hits.size();
     const Admission a = s.rs->admit(to_admit, busy, true, eviction_cap(layer));
     xst_.deferred += uint64_t(a.deferred);
-    // exclusive: the victims go back to free blocks first; only a copy into a written-back victim's slot waits
-    size_t n_wb = 0;
-    cudaEvent_t wb_ev = excl_ && !a.evicted.empty() ? write_back(layer, a, &n_wb) : nullptr;
-    for (size_t k = 0; k < a.admitted.size(); ++k) {
-      cudaEvent_t wait = nullptr;
-      for (size_t i = 0; wb_ev && i < n_wb && !wait; ++i)
-        if (a.evicted_slot[i] == a.slot_of[k]) wait = wb_ev;
-      fetch_into_persistent(layer, a.admitted[k], a.slot_of[k], wait);
-    }
+    fetch_admitted(layer, a);
     for (int32_t u : a.transient)
       if (!fetch_into_ring(layer, u)) {
         s.pending.push_back(u);
@@ -837,6 +943,8 @@ class HostCtx final : public HostContext {
     require(!(excl_ && o_.exclusive_discard && d_.tiers == Tiers::Pinned), SS_E_INVALID,
             "open: exclusive_discard needs a descriptor whose tiers allow disk (tiers = \"pinned\" refuses it)");
     require(o_.readahead_units == 0, SS_E_UNSUPPORTED, "open: host read-ahead is not in this build");
+    require(!o_.spec_persistent, SS_E_UNSUPPORTED,
+            "open: spec_persistent is not in this build (speculative prefetches take the stream ring)");
     ck(cudaSetDevice(o_.device), "cudaSetDevice");
     ck_launch_preload();
     ck(cudaStreamCreateWithFlags(&copy_, cudaStreamNonBlocking), "cudaStreamCreate (copy)");
@@ -949,6 +1057,7 @@ class HostCtx final : public HostContext {
       s.slot.assign(size_t(l.n_units), -1);
       s.job.assign(size_t(l.n_units), nullptr);
       s.count.assign(size_t(l.n_units), 0);
+      s.spec_unclaimed.assign(size_t(l.n_units), 0);
     }
     for (const tsb::RingClass& rc : plan_.rings) {
       if (!rc.slots) continue;
@@ -1091,7 +1200,7 @@ class HostCtx final : public HostContext {
   std::mutex copy_mu_;
   std::mutex q_mu_;
   std::condition_variable q_cv_, done_cv_;
-  std::deque<JobPtr> queue_;
+  std::deque<JobPtr> queue_, spec_queue_;
   std::vector<std::thread> workers_;
   bool stop_ = false;
   std::vector<JobPtr> batch_, fwd_jobs_;
@@ -1099,7 +1208,7 @@ class HostCtx final : public HostContext {
   std::vector<ss_layer_stats> stats_, fwd_;
   ss_stats_hook hook_ = nullptr;
   void* hook_user_ = nullptr;
-  bool in_fwd_ = false, poisoned_ = false, stream_set_ = false;
+  bool in_fwd_ = false, fwd_open_ = false, poisoned_ = false, stream_set_ = false;
   void* stream_ = nullptr;
   uint64_t forwards_ = 0, ce_min_ = 0, land_launches_ = 0;
   // exclusive tier mode

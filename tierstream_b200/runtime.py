@@ -171,6 +171,14 @@ class HostContext:
     def layer_all(self, layer):
         abi.check(abi.load().ss_layer_all(self.h, layer))
 
+    def prefetch(self, layer, ids, speculative=False):
+        a = np.ascontiguousarray(ids, dtype=np.int32)
+        abi.check(abi.load().ss_prefetch(self.h, layer, a.ctypes.data_as(C.POINTER(C.c_int32)), a.size,
+                                         1 if speculative else 0))
+
+    def prefetch_layer(self, layer):
+        abi.check(abi.load().ss_prefetch_layer(self.h, layer))
+
     def acquire(self, layer, stream):
         v = abi.ss_layer_view()
         abi.check(abi.load().ss_acquire(self.h, layer, stream, C.byref(v)))
