@@ -29,6 +29,7 @@
 #include "errors.hpp"
 #include "kernels.hpp"
 #include "peer.hpp"
+#include "pinned.hpp"
 #include "source_file.hpp"
 #include "xxh64.hpp"
 
@@ -1282,43 +1283,19 @@ class CudaDgContext final : public DgContext {
     }
     gpu_wait_us_.assign(G, -1);
     gpu_ready_us_.assign(G, -1);
-    // pinned blocks (mapped: the land kernel reads them), <= 1 GiB chunks allocated by a pool of threads (pinning the
-    // pages is the open's longest step, and the driver pins chunks of different threads side by side); the reset
-    // staging unit
+    // pinned blocks (mapped: the land kernel reads them) in <= 1 GiB chunks (pinned.cu: mapped, populated by a pool of
+    // threads with huge pages, registered); the reset staging unit
     const uint64_t hs = x_.host_stride;
     const uint64_t per_chunk = std::max<uint64_t>(1, (uint64_t(1) << 30) / hs);
     std::vector<uint64_t> chunk_units;
+    std::vector<size_t> chunk_bytes;
     for (uint64_t left = peer_ && peer_->all_owned ? 0 : x_.blocks; left > 0;) {
       chunk_units.push_back(std::min(per_chunk, left));
+      chunk_bytes.push_back(size_t(chunk_units.back() * hs));
       left -= chunk_units.back();
     }
-    chunks_.assign(chunk_units.size(), nullptr);
-    {
-      std::atomic<size_t> next{0};
-      std::mutex err_mu;
-      std::string err;
-      const size_t nth = std::min<size_t>(chunk_units.size(), 8);
-      std::vector<std::thread> th;
-      for (size_t t = 0; t < nth; ++t)
-        th.emplace_back([&] {
-          if (cudaSetDevice(device_) != cudaSuccess) return;
-          for (;;) {
-            const size_t i = next.fetch_add(1);
-            if (i >= chunk_units.size()) return;
-            void* p = nullptr;
-            const cudaError_t e = cudaHostAlloc(&p, size_t(chunk_units[i] * hs), cudaHostAllocMapped | cudaHostAllocPortable);
-            if (e != cudaSuccess) {
-              (void)cudaGetLastError();
-              std::lock_guard<std::mutex> lk(err_mu);
-              if (err.empty()) err = std::string("cudaHostAlloc (blocks): ") + cudaGetErrorString(e);
-              return;
-            }
-            chunks_[i] = p;
-          }
-        });
-      for (auto& t : th) t.join();
-      if (!err.empty()) fail(SS_E_NOMEM, "device-gated: " + err);
-    }
+    pinned_ = alloc_pinned(chunk_bytes, device_);
+    for (const PinnedChunk& c : pinned_) chunks_.push_back(c.ptr);
     for (size_t c = 0; c < chunks_.size(); ++c) {
       void* pd = nullptr;
       ck(cudaHostGetDevicePointer(&pd, chunks_[c], 0), "cudaHostGetDevicePointer (blocks)");
@@ -1538,8 +1515,8 @@ class CudaDgContext final : public DgContext {
     if (ctl_) cudaFree(ctl_);
     if (mapped_h_) cudaFreeHost(mapped_h_);
     if (stamps_h_) cudaFreeHost(stamps_h_);
-    for (void* c : chunks_)
-      if (c) cudaFreeHost(c);
+    free_pinned(pinned_);
+    chunks_.clear();
     if (bufs_.staging) cudaFreeHost(bufs_.staging);
   }
 
@@ -1553,7 +1530,8 @@ class CudaDgContext final : public DgContext {
   uint32_t* ctl_ = nullptr;
   void* mapped_h_ = nullptr;
   unsigned long long* stamps_h_ = nullptr;
-  std::vector<void*> chunks_;
+  std::vector<void*> chunks_;       // the block chunks' host addresses
+  std::vector<PinnedChunk> pinned_;  // their allocation
   dev::DgDev dev_{};
   Mapped m_;
   std::unique_ptr<CudaMover> mover_;

@@ -33,6 +33,7 @@
 #include "ctx.hpp"
 #include "errors.hpp"
 #include "kernels.hpp"
+#include "pinned.hpp"
 #include "resident_set.hpp"
 #include "source_file.hpp"
 #include "xxh64.hpp"
@@ -961,10 +962,11 @@ class HostCtx final : public HostContext {
     // pinned tier (the planner's layout, mapped: the land kernel reads it)
     pinned_of_.assign(size_t(d_.total_units), nullptr);
     const PinnedLayout pl = pinned_layout(d_, plan_.tier);
-    for (uint64_t bytes : pl.chunk_bytes) {
-      void* p = nullptr;
-      ck(cudaHostAlloc(&p, size_t(bytes), cudaHostAllocMapped | cudaHostAllocPortable), "cudaHostAlloc (pinned tier)");
-      chunks_.push_back(p);
+    {
+      std::vector<size_t> sizes;
+      for (uint64_t bytes : pl.chunk_bytes) sizes.push_back(size_t(bytes));
+      pinned_ = alloc_pinned(sizes, o_.device);  // pinned.cu: mapped, populated in parallel, huge pages
+      for (const PinnedChunk& c : pinned_) chunks_.push_back(c.ptr);
     }
     for (int64_t g = 0; g < d_.total_units; ++g)
       if (pl.chunk_of[size_t(g)] >= 0) pinned_of_[size_t(g)] = at(chunks_[size_t(pl.chunk_of[size_t(g)])], pl.offset_of[size_t(g)]);
@@ -994,14 +996,17 @@ class HostCtx final : public HostContext {
         const uint64_t per_chunk = std::max<uint64_t>(1, (uint64_t(1) << 30) / bytes);
         free_blocks_[k].reserve(size_t(class_total[k] + plan_.spares[k].blocks));  // never reallocates later
         std::vector<char*> blocks;
+        std::vector<size_t> sizes;
+        std::vector<uint64_t> units;
         for (uint64_t left = plan_.spares[k].blocks; left > 0;) {
-          const uint64_t n = std::min(per_chunk, left);
-          void* chunk = nullptr;
-          ck(cudaHostAlloc(&chunk, size_t(n * bytes), cudaHostAllocMapped | cudaHostAllocPortable),
-             "cudaHostAlloc (spare blocks)");
-          spare_chunks_.push_back(chunk);
-          for (uint64_t i = 0; i < n; ++i) blocks.push_back(at(chunk, i * bytes));
-          left -= n;
+          units.push_back(std::min(per_chunk, left));
+          sizes.push_back(size_t(units.back() * bytes));
+          left -= units.back();
+        }
+        std::vector<PinnedChunk> got = alloc_pinned(sizes, o_.device);
+        for (size_t c = 0; c < got.size(); ++c) {
+          for (uint64_t i = 0; i < units[c]; ++i) blocks.push_back(at(got[c].ptr, i * bytes));
+          spare_pinned_.push_back(got[c]);
         }
         for (size_t i = blocks.size(); i-- > 0;) free_blocks_[k].push_back(blocks[i]);
         xst_.free_blocks += plan_.spares[k].blocks;
@@ -1163,10 +1168,9 @@ class HostCtx final : public HostContext {
     L_.clear();
     for (void* b : ring_bases_) cudaFree(b);
     ring_bases_.clear();
-    for (void* c : chunks_) cudaFreeHost(c);
+    free_pinned(pinned_);
     chunks_.clear();
-    for (void* c : spare_chunks_) cudaFreeHost(c);
-    spare_chunks_.clear();
+    free_pinned(spare_pinned_);
     if (wb_stream_) cudaStreamDestroy(wb_stream_);
     wb_stream_ = nullptr;
     if (blocks_ev_) cudaEventDestroy(blocks_ev_);
@@ -1190,7 +1194,8 @@ class HostCtx final : public HostContext {
   std::vector<RingClass> rings_;
   std::vector<void*> ring_bases_;
   std::vector<cudaEvent_t> ring_owner_ev_;
-  std::vector<void*> chunks_;
+  std::vector<void*> chunks_;       // the pinned tier's chunks (host addresses)
+  std::vector<PinnedChunk> pinned_;  // their allocation
   std::vector<const char*> pinned_of_;
   std::vector<char*> staging_;
   std::vector<size_t> st_free_;
@@ -1220,7 +1225,7 @@ class HostCtx final : public HostContext {
   std::vector<cudaEvent_t> wb_evs_;
   std::vector<int> layer_class_;                 // per layer: its block class (-1: none)
   std::vector<std::vector<char*>> free_blocks_;  // per class, the lowest address last (taken first)
-  std::vector<void*> spare_chunks_;
+  std::vector<PinnedChunk> spare_pinned_;
   ss_exclusive_stats xst_{};
 };
 
