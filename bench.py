@@ -413,7 +413,11 @@ def main():
                      "unit": "GB/s", "frac": round(achieved / peak, 4) if achieved and peak else None, "traffic": None,
                      "peak_source": "measured in this run: copy-engine pinned->HBM 1 GiB, best of 5 "
                                     "(MEASURED_PEAKS.json has no host-link figure)",
-                     "algorithmic_bytes": moved, "device_ms": round(dma_ms, 3)},
+                     "algorithmic_bytes": moved, "device_ms": round(dma_ms, 3),
+                     "traffic_note": "the demand copies of 33 MB parts run on the copy engines (peer-tier pulls on "
+                                     "the land kernel), whose DRAM bytes ncu does not attribute to one kernel; the land "
+                                     "kernel's own captures (profiles/land_kernel_*.md) show DRAM traffic at or below "
+                                     "its algorithmic bytes"},
         "gpu_launches": int(a.steps * (2 + 2 * LAYERS) + land_launches + a.steps * LAYERS),
         "clocks": clk, "open_s": round(t_open, 2), "open": open_stats, "dg": dg, "miss_layer_path": layer_path,
         "options": {"wb_defer": a.wb_defer, "wb_stream": a.wb_stream, "spare_slots_per_layer": a.spare,
