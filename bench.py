@@ -415,9 +415,9 @@ def main():
                                     "(MEASURED_PEAKS.json has no host-link figure)",
                      "algorithmic_bytes": moved, "device_ms": round(dma_ms, 3),
                      "traffic_note": "the demand copies of 33 MB parts run on the copy engines (peer-tier pulls on "
-                                     "the land kernel), whose DRAM bytes ncu does not attribute to one kernel; the land "
-                                     "kernel's own captures (profiles/land_kernel_*.md) show DRAM traffic at or below "
-                                     "its algorithmic bytes"},
+                                     "the land kernel), whose DRAM bytes ncu does not attribute to one kernel; ncu "
+                                     "captures of the land kernel alone show DRAM traffic at or below its algorithmic "
+                                     "bytes"},
         "gpu_launches": int(a.steps * (2 + 2 * LAYERS) + land_launches + a.steps * LAYERS),
         "clocks": clk, "open_s": round(t_open, 2), "open": open_stats, "dg": dg, "miss_layer_path": layer_path,
         "options": {"wb_defer": a.wb_defer, "wb_stream": a.wb_stream, "spare_slots_per_layer": a.spare,
