@@ -45,6 +45,8 @@ def ref():
     global _ref
     if _ref is None and ref_available():
         lib = C.CDLL(os.path.join(HERE, "_ref", "libtsref.so"))
+        lib.oref_copy_threads.restype = C.c_uint
+        lib.oref_copy_threads.argtypes = []
         lib.oref_xxh64.restype = C.c_uint64
         lib.oref_xxh64.argtypes = [C.c_void_p, C.c_size_t, C.c_uint64]
         lib.oref_host_replay.restype = C.c_int

@@ -2,10 +2,12 @@
 // way its DgService::serve_token drives it (dg_service.cpp:269-365), with a host transport in the pattern of its
 // tests' immediate transport (tests/test_dg_service.cpp:33-85): every event complete when queried, copies done at
 // once. The product library never links this file.
+#include <algorithm>
 #include <cstdint>
 #include <cstdio>
 #include <cstring>
 #include <exception>
+#include <thread>
 #include <vector>
 
 #include "dg_core.hpp"
@@ -13,6 +15,28 @@
 #include "xxh64.hpp"
 
 namespace {
+
+// Copies of the host transport on every host thread (the timed baseline uses what the machine has): pieces of at
+// least 4 MiB each, one thread per piece.
+unsigned copy_threads() {
+  static const unsigned n = std::max(1u, std::min(32u, std::thread::hardware_concurrency()));
+  return n;
+}
+void pcopy(void* dst, const void* src, size_t n) {
+  const unsigned t = std::min<unsigned>(copy_threads(), unsigned(std::max<size_t>(1, n >> 22)));
+  if (t <= 1) {
+    std::memcpy(dst, src, n);
+    return;
+  }
+  const size_t per = (n / t + 4095) / 4096 * 4096;
+  std::vector<std::thread> th;
+  for (unsigned i = 0; i < t; ++i) {
+    const size_t lo = size_t(i) * per, hi = std::min(n, lo + per);
+    if (lo >= hi) break;
+    th.emplace_back([=] { std::memcpy(static_cast<char*>(dst) + lo, static_cast<const char*>(src) + lo, hi - lo); });
+  }
+  for (auto& x : th) x.join();
+}
 
 class HostTransport final : public ts::DgTransport {
  public:
@@ -35,10 +59,10 @@ class HostTransport final : public ts::DgTransport {
   }
   uint32_t alias_slots_ = 1, alias_blocks_ = 1;
   void h2d(Stream, int32_t slot, int32_t block) override {
-    if (move_) std::memcpy(slot_ptr(slot), block_ptr(block), unit_);
+    if (move_) pcopy(slot_ptr(slot), block_ptr(block), unit_);
   }
   void d2h(int32_t slot, int32_t block) override {
-    if (move_) std::memcpy(block_ptr(block), slot_ptr(slot), unit_);
+    if (move_) pcopy(block_ptr(block), slot_ptr(slot), unit_);
   }
   void d2d(int32_t src, int32_t dst) override {
     if (move_) std::memmove(slot_ptr(dst), slot_ptr(src), unit_);
@@ -50,7 +74,7 @@ class HostTransport final : public ts::DgTransport {
     if (!move_) return;
     uint64_t off = 0;
     for (uint32_t i = 0; i < p; ++i) off += parts_[i];
-    std::memcpy(block_ptr(block) + off, slot_ptr(slot) + off, parts_[p]);
+    pcopy(block_ptr(block) + off, slot_ptr(slot) + off, parts_[p]);
   }
   uint32_t parts() const override { return uint32_t(parts_.size()); }
   uint64_t part_bytes(uint32_t p) const override { return parts_[p]; }
@@ -161,3 +185,5 @@ extern "C" __attribute__((visibility("default"))) int oref_dg_replay(const oref_
     return -1;
   }
 }
+
+extern "C" __attribute__((visibility("default"))) unsigned oref_copy_threads(void) { return copy_threads(); }
