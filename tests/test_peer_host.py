@@ -131,3 +131,44 @@ def test_replan_entry_points_refuse_bad_arguments():
     bases = (C.c_void_p * 1)()
     assert lib.tsb_peer_store_migrate(None, owner, bases, 4, 1, None, None, None, None) == abi.SS_E_INVALID
     assert b"null argument" in lib.ss_last_error()
+
+
+def _rank_dies(rank, world, port, out_dir):
+    import datetime
+
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=5))
+    try:
+        counts = peer.all_reduce_counts(np.ones(8, dtype=np.int64), dist)
+        if rank == 1:
+            raise SystemExit(3)  # the rank leaves between the steps, before the handle exchange
+        try:
+            peer.all_gather_handles(bytes(64), dist, world)
+            outcome = "returned"
+        except Exception as e:  # the survivor learns of it from the collective's timeout, not a hang
+            outcome = "raised: " + type(e).__name__
+        with open(os.path.join(out_dir, "r%d.txt" % rank), "w") as f:
+            f.write("%s %d" % (outcome, int(counts.sum())))
+    finally:
+        if rank == 0:
+            try:
+                dist.destroy_process_group()
+            except Exception:
+                pass
+
+
+def test_a_rank_that_leaves_fails_the_exchange_with_an_error(tmp_path):
+    import socket
+
+    import torch.multiprocessing as mp
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    ctx = mp.start_processes(_rank_dies, args=(2, port, str(tmp_path)), nprocs=2, start_method="spawn", join=False)
+    ctx.processes[1].join(60)
+    ctx.processes[0].join(60)
+    assert ctx.processes[1].exitcode == 3
+    text = (tmp_path / "r0.txt").read_text()
+    assert text.startswith("raised:") and text.endswith(" 16"), text
