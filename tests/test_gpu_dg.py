@@ -161,3 +161,32 @@ def test_context_on_another_device_keeps_the_callers_device(small_model):
         torch.cuda.set_device(1)
         run.close()
         torch.cuda.set_device(0)
+
+
+@pytest.mark.parametrize("wb_defer", [0, 1])
+def test_predictions_tables_match_reference(small_model, orc, ref, monkeypatch, wb_defer):
+    """Next-layer predictions (ss_dg_enqueue_predict) under the deterministic schedule: the prefetches the service
+    issues from them, and so the slot table after every token, equal the reference DgCore's replay with the same
+    predictions; every routed unit's bytes are the source's."""
+    monkeypatch.setenv("TSB_DG_DETERMINISTIC", "1")
+    m = small_model
+    ids = synth.zipf_trace(30, m.layers, m.units, 2, s=0.9, seed=15)
+    preds = synth.zipf_trace(30, m.layers, m.units, 2, s=0.9, seed=16)
+    run = harness.DgRun(m, residents_per_layer=3, max_ids=2, n_pred=2, wb_defer=wb_defer)
+    try:
+        P = m.layers * m.units - len(run.resident_keys)
+        cfg = runtime.replay_config([m.units] * m.layers, list(m.part_bytes),
+                                    persistent_slots=len(run.resident_keys) + m.layers, bank_slots=2,
+                                    blocks=P + m.layers, spare_target=m.layers, order=run.resident_keys,
+                                    tokens=ids.shape[0], n_ids=2, n_pred=2, wb_defer=wb_defer)
+        t_ref, s_ref = oracle.ref_replay(cfg, ids, preds)
+        want = expected_sums(m, orc)
+        for t in range(ids.shape[0]):
+            got = run.step(ids[t], preds[t])
+            keys = np.arange(m.layers)[:, None] * m.units + ids[t]
+            assert np.array_equal(got, want[keys]), "token %d read wrong bytes" % t
+            assert np.array_equal(run.ctx.table(run.keys), t_ref[t]), "slot table differs after token %d" % t
+        st = run.ctx.stats()
+        assert st["prefetched"] == s_ref[-1][5] and st["prefetched"] > 0
+    finally:
+        run.close()
