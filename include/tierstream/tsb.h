@@ -11,7 +11,7 @@
 extern "C" {
 #endif
 
-/* ---- K1 / K4 / K5: batched copies (the land kernel) ----
+/* ---- K1 / K5: batched copies (the land kernel) ----
  * n copies of bytes[i] bytes from src[i] to dst[i] in one launch (copies must not overlap each other; any side may be
  * device memory, mapped pinned host memory or a peer device's memory). Then, when n_entries > 0, slot_of[keys[j]] =
  * vals[j], and when ready_word is not NULL, *ready_word = ready_val, published once every copy landed. counter: one
@@ -21,6 +21,17 @@ extern "C" {
 SS_API ss_status tsb_land(const void* const* src, void* const* dst, const uint64_t* bytes, uint32_t n,
                           int32_t* slot_of, const uint32_t* keys, const int32_t* vals, uint32_t n_entries,
                           uint32_t* ready_word, uint32_t ready_val, uint32_t* counter, uint32_t blocks, void* stream);
+
+/* ---- K4: HBM -> HBM moves through shared memory (TMA bulk copies) ----
+ * The same batch as tsb_land, every copy device memory to device memory with 16-byte aligned addresses and 16-byte
+ * multiple sizes (else SS_E_INVALID): each 64 KiB chunk a bulk load into shared memory and a bulk store out, three
+ * chunks in flight per CTA, one CTA per SM. What reset compaction (ss_dg_reset_open) runs. tsb_move_timeouts: the
+ * chunk loads that did not complete within 2 s since the last call (their batch publishes nothing), then reset; -1 on
+ * a device error. */
+SS_API ss_status tsb_move(const void* const* src, void* const* dst, const uint64_t* bytes, uint32_t n,
+                          int32_t* slot_of, const uint32_t* keys, const int32_t* vals, uint32_t n_entries,
+                          uint32_t* ready_word, uint32_t ready_val, uint32_t* counter, uint32_t blocks, void* stream);
+SS_API int tsb_move_timeouts(void);
 
 /* ---- K3: device xxh64 of whole units ----
  * Unit i is n_spans[i] (1..4) spans spans[4 i + s] of span_bytes[4 i + s] bytes hashed back to back (a gated unit's

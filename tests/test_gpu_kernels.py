@@ -152,3 +152,57 @@ def test_device_xxh64_many_units_random_layouts(orc):
     assert pos < h.size
     got, _ = xxh_units(units)
     assert [int(x) for x in got] == want
+
+
+def test_move_kernel_copies_and_publishes():
+    """K4 (tsb_move): HBM -> HBM batches through shared memory by TMA bulk copies, 16-byte aligned copies of assorted
+    sizes (below, at and above the 64 KiB chunk, many in one batch), then the entries and the ready word published, on
+    two launches in a row with the same completion counter."""
+    rng = np.random.default_rng(7)
+    plans = []
+    for rep in range(2):
+        plan, pos = [], 0
+        for size in [16, 4096, 65520, 65536, 65552, 1 << 20, 3 * (1 << 20) + 48] + [4096 * int(x) for x in
+                                                                                      rng.integers(1, 64, size=200)]:
+            plan.append((pos, pos, size))
+            pos += (size + 255) // 256 * 256
+        plans.append((plan, pos))
+    total = max(pos for _, pos in plans)
+    src = torch.from_numpy(rng.integers(0, 256, size=total, dtype=np.uint8)).cuda()
+    dst = torch.zeros(total, dtype=torch.uint8, device="cuda")
+    table = torch.full((64,), -1, dtype=torch.int32, device="cuda")
+    words = torch.zeros(4, dtype=torch.int32, device="cuda")  # [0] ready, [1] counter
+    s = torch.cuda.Stream()
+    lib = abi.load()
+    for rep, (plan, pos) in enumerate(plans):
+        assert pos <= src.numel() and pos <= dst.numel()
+        dst.zero_()
+        n = len(plan)
+        sp = (C.c_void_p * n)(*[src.data_ptr() + a for a, _, _ in plan])
+        dp = (C.c_void_p * n)(*[dst.data_ptr() + b for _, b, _ in plan])
+        by = (C.c_uint64 * n)(*[z for *_, z in plan])
+        assert n <= 384 and all(a + z <= total and a % 16 == 0 and z % 16 == 0 for a, _, z in plan)
+        s.wait_stream(torch.cuda.current_stream())
+        keys = (C.c_uint32 * 3)(3, 9, 60)
+        vals = (C.c_int32 * 3)(7 + rep, 8 + rep, 9 + rep)
+        abi.check(lib.tsb_move(sp, dp, by, n, C.c_void_p(table.data_ptr()), keys, vals, 3,
+                               C.c_void_p(words.data_ptr()), 41 + rep, C.c_void_p(words.data_ptr() + 4), 0,
+                               s.cuda_stream))
+        s.synchronize()
+        assert lib.tsb_move_timeouts() == 0
+        h, d = src.cpu().numpy(), dst.cpu().numpy()
+        for a, b, z in plan:
+            assert np.array_equal(d[b:b + z], h[a:a + z]), "copy of %d bytes differs" % z
+        t = table.cpu().numpy()
+        assert t[3] == 7 + rep and t[9] == 8 + rep and t[60] == 9 + rep
+        assert int(words[0].item()) == 41 + rep and int(words[1].item()) == 0  # the counter is back at zero
+
+
+def test_move_kernel_refuses_unaligned():
+    lib = abi.load()
+    src = torch.zeros(1024, dtype=torch.uint8, device="cuda")
+    sp = (C.c_void_p * 1)(src.data_ptr() + 8)
+    dp = (C.c_void_p * 1)(src.data_ptr() + 512)
+    by = (C.c_uint64 * 1)(64)
+    st = lib.tsb_move(sp, dp, by, 1, None, None, None, 0, None, 0, None, 0, None)
+    assert st == abi.SS_E_INVALID and b"multiple of 16" in lib.ss_last_error()

@@ -205,6 +205,8 @@ _PROTOS = {
     "ss_test_dg_mutate": (C.c_int, [vp, C.c_int]),
     "ss_test_dg_stop_service": (C.c_int, [vp]),
     "tsb_land": (C.c_int, [P(vp), P(vp), P(u64), u32, vp, P(u32), P(i32), u32, vp, u32, vp, u32, vp]),
+    "tsb_move": (C.c_int, [P(vp), P(vp), P(u64), u32, vp, P(u32), P(i32), u32, vp, u32, vp, u32, vp]),
+    "tsb_move_timeouts": (C.c_int, []),
     "tsb_xxh64_units": (C.c_int, [P(vp), P(u64), P(u32), u32, vp, vp, vp, vp, vp]),
     "tsb_xxh64_units_static": (C.c_int, [P(vp), P(u64), P(u32), u32, vp, vp, vp, vp]),
     "tsb_peer_plan": (C.c_int, [P(u64), u32, u32, P(u64), P(C.c_int32)]),

@@ -319,15 +319,40 @@ class CudaMover final : public Mover {
     flush(kDem);
     uint32_t max_wave = 0;
     for (uint32_t w : wave) max_wave = std::max(max_wave, w);
-    for (uint32_t w = 0; w <= max_wave; ++w) {  // one or more land launches per wave, stream-ordered on kDem
+    // K4 (TMA bulk copies through shared memory) per wave, stream-ordered on kDem; the arena's parts are 256-byte
+    // multiples, so every move fits it (the land kernel takes one that does not, on the same stream)
+    auto mb = std::make_unique<dev::Batch>();
+    uint64_t chunks = 0;
+    auto launch = [&] {
+      if (!mb->n_copies) return;
+      ck_launch(dev::launch_move(*mb, int(std::min<uint64_t>(std::max<uint64_t>(chunks, 1), 148)), s_[kDem]),
+                "move kernel");
+      ++launches_;
+      mb->n_copies = 0;
+      chunks = 0;
+    };
+    for (uint32_t w = 0; w <= max_wave; ++w) {
       for (size_t i = 0; i < moves.size(); ++i) {
         if (wave[i] != w) continue;
-        for (uint32_t p = 0; p < parts(); ++p)
-          add_copy(kDem, arena(p, moves[i].first), arena(p, moves[i].second), x_.part_bytes[p]);
+        for (uint32_t p = 0; p < parts(); ++p) {
+          const char* src = arena(p, moves[i].first);
+          char* dst = arena(p, moves[i].second);
+          if (((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst) | x_.part_bytes[p]) & 15u) != 0) {
+            add_copy(kDem, src, dst, x_.part_bytes[p]);
+            continue;
+          }
+          if (mb->n_copies == dev::kMaxCopies) launch();
+          mb->copies[mb->n_copies++] = {src, dst, x_.part_bytes[p]};
+          chunks += (x_.part_bytes[p] + (64u << 10) - 1) >> 16;
+        }
       }
-      flush(kDem);
+      flush(kDem);  // the wave's copies, if any, that the move kernel cannot take
+      launch();
     }
     sync(kDem);
+    uint32_t timeouts = 0;
+    ck_launch(dev::move_take_timeouts(&timeouts), "move kernel timeout word");
+    require(!timeouts, SS_E_BACKEND, "device-gated: a staging copy of the move kernel did not complete");
   }
   void h2h(int32_t src, int32_t dst, uint32_t key) override {
     if (peer_ && peer_->owned(key)) return;

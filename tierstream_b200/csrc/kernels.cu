@@ -1,5 +1,6 @@
 // Device kernels of the B200 runtime (sm_100a). Byte movement and control only: no tensor-core work exists on this
 // path. See kernels.hpp for the launch contracts.
+#include <atomic>
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -11,7 +12,7 @@ namespace dev {
 namespace {
 
 // ---------------------------------------------------------------------------------------------------------------
-// K1 / K4 / K5: the batched copy ("land") kernel.
+// K1 / K5: the batched copy ("land") kernel.
 // The copies are cut into 64 KiB chunks; block i takes chunks i, i + grid, ... Each chunk moves 16-byte vectors with
 // eight loads in flight per thread (mapped pinned host memory is read over PCIe, HBM or a peer over NVLink). The last
 // block to finish publishes the batch's entries and ready word, so one launch replaces a copy per part plus a stream
@@ -341,6 +342,106 @@ __global__ __launch_bounds__(32) void xxh64_kernel(const HashUnit* __restrict__ 
 }
 
 // ---------------------------------------------------------------------------------------------------------------
+// K4: HBM -> HBM moves staged through shared memory by TMA bulk copies (reset compaction). One warp per CTA, its lane 0
+// issuing: every 64 KiB chunk is a bulk load global -> shared (completing on the stage's mbarrier) followed by a bulk
+// store shared -> global, through a ring of 3 stages, with the loads of the next two chunks in flight while a store
+// drains. Copies must be 16-byte aligned with 16-byte multiple sizes (the host checks; the land kernel takes the
+// rest). The last CTA publishes entries and the ready word as K1 does. A load wait that runs out (2 s) is counted in
+// g_move_timeouts; that CTA waits (bounded) for its loads in flight and for its stores, and leaves without
+// publishing, so the batch's publication never happens and the host reports the failure.
+// ---------------------------------------------------------------------------------------------------------------
+constexpr int kMoveStages = 3;
+constexpr uint32_t kMoveChunk = 64u << 10;
+constexpr size_t kMoveSmem = size_t(kMoveStages) * kMoveChunk + kMoveStages * 8;
+
+__device__ uint32_t g_move_timeouts;
+
+__device__ __forceinline__ void bulk_store(void* gdst, const void* ssrc, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(gdst), "r"(smem_addr(ssrc)),
+               "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_reads() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+__global__ __launch_bounds__(32) void move_kernel(const __grid_constant__ Batch b) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ uint32_t first_chunk[kMaxCopies + 1];
+  if (threadIdx.x != 0) return;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + size_t(kMoveStages) * kMoveChunk);
+  uint32_t acc = 0;
+  for (uint32_t c = 0; c < b.n_copies; ++c) {
+    first_chunk[c] = acc;
+    acc += uint32_t((b.copies[c].bytes + kMoveChunk - 1) / kMoveChunk);
+  }
+  first_chunk[b.n_copies] = acc;
+  const uint32_t total = acc;
+  const uint32_t mine = blockIdx.x < total ? (total - blockIdx.x + gridDim.x - 1) / gridDim.x : 0u;
+  for (int st = 0; st < kMoveStages; ++st) mbar_init(bars + st, 1);
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  // chunk j of this CTA: global chunk blockIdx.x + j * gridDim.x; the copy index only grows with j
+  uint32_t load_c = 0, store_c = 0;
+  auto locate = [&](uint32_t j, uint32_t& c, const uint8_t*& src, uint8_t*& dst, uint32_t& n) {
+    const uint32_t k = blockIdx.x + j * gridDim.x;
+    while (c + 1 < b.n_copies && first_chunk[c + 1] <= k) ++c;
+    const uint64_t off = uint64_t(k - first_chunk[c]) * kMoveChunk;
+    const uint64_t left = b.copies[c].bytes - off;
+    n = uint32_t(left < kMoveChunk ? left : kMoveChunk);
+    src = static_cast<const uint8_t*>(b.copies[c].src) + off;
+    dst = static_cast<uint8_t*>(b.copies[c].dst) + off;
+  };
+  auto issue_load = [&](uint32_t j) {
+    const uint8_t* src;
+    uint8_t* dst;
+    uint32_t n;
+    locate(j, load_c, src, dst, n);
+    uint64_t* bar = bars + (j % kMoveStages);
+    mbar_arrive_expect_tx(bar, n);
+    bulk_load(smem + size_t(j % kMoveStages) * kMoveChunk, src, n, bar);
+  };
+  for (uint32_t j = 0; j < uint32_t(kMoveStages) && j < mine; ++j) issue_load(j);
+  bool ok = true;
+  uint32_t j = 0;
+  for (; j < mine; ++j) {
+    if (!mbar_wait(bars + (j % kMoveStages), (j / kMoveStages) & 1u)) {
+      ok = false;
+      break;
+    }
+    const uint8_t* src;
+    uint8_t* dst;
+    uint32_t n;
+    locate(j, store_c, src, dst, n);
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    bulk_store(dst, smem + size_t(j % kMoveStages) * kMoveChunk, n);
+    bulk_commit();
+    if (j + kMoveStages < mine) {
+      bulk_wait_reads();  // the stage is free once the store has read it
+      issue_load(j + kMoveStages);
+    }
+  }
+  if (!ok) {
+    atomicAdd(&g_move_timeouts, 1u);
+    for (uint32_t k = j; k < mine && k < j + kMoveStages; ++k)
+      (void)mbar_wait(bars + (k % kMoveStages), (k / kMoveStages) & 1u);
+    bulk_wait_all();
+    return;
+  }
+  bulk_wait_all();  // every store of this CTA has landed
+  if (!b.done_counter) return;
+  asm volatile("fence.proxy.async;" ::: "memory");
+  __threadfence();
+  if (atomicAdd(b.done_counter, 1u) != gridDim.x - 1) return;
+  __threadfence();
+  for (uint32_t e = 0; e < b.n_entries; ++e)
+    asm volatile("st.relaxed.sys.global.s32 [%0], %1;" ::"l"(b.slot_of + b.entry_key[e]), "r"(b.entry_val[e])
+                 : "memory");
+  __threadfence_system();
+  *b.done_counter = 0;
+  if (b.ready_word) asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(b.ready_word), "r"(b.ready_val) : "memory");
+}
+
+// ---------------------------------------------------------------------------------------------------------------
 // K2: device-gated decode control. The words they share with the service thread follow the reference's protocol
 // (dg_kernels.cu:41-135): begin authorizes one sequence; export writes the record and flag; wait polls the ready
 // word; end folds the errors and writes done. Here ready lives in device memory (written by the land kernel or a
@@ -479,6 +580,42 @@ int launch_batch(const Batch& b, int blocks, void* stream) {
   if (blocks < 1) blocks = 1;
   batch_kernel<<<blocks, kCopyThreads, 0, static_cast<cudaStream_t>(stream)>>>(b);
   return last_error();
+}
+
+bool move_fits(const Batch& b) {
+  for (uint32_t i = 0; i < b.n_copies; ++i)
+    if (((reinterpret_cast<uintptr_t>(b.copies[i].src) | reinterpret_cast<uintptr_t>(b.copies[i].dst) |
+          uintptr_t(b.copies[i].bytes)) & 15u) != 0)
+      return false;
+  return true;
+}
+
+int launch_move(const Batch& b, int blocks, void* stream) {
+  if (b.n_copies > kMaxCopies || b.n_entries > kMaxEntries || !move_fits(b)) return int(cudaErrorInvalidValue);
+  // the shared-memory attribute is a per-device setting of the kernel
+  static std::atomic<uint64_t> set_on{0};
+  int device = 0;
+  if (const cudaError_t e = cudaGetDevice(&device); e != cudaSuccess) return int(e);
+  const uint64_t bit = device < 64 ? uint64_t(1) << device : 0;
+  if (!bit || !(set_on.load() & bit)) {
+    const cudaError_t e = cudaFuncSetAttribute(move_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kMoveSmem));
+    if (e != cudaSuccess) return int(e);
+    set_on.fetch_or(bit);
+  }
+  if (blocks < 1) blocks = 1;
+  move_kernel<<<blocks, 32, kMoveSmem, static_cast<cudaStream_t>(stream)>>>(b);
+  return last_error();
+}
+
+int move_take_timeouts(uint32_t* out) {
+  uint32_t v = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&v, g_move_timeouts, sizeof v);
+  if (e == cudaSuccess && v) {
+    const uint32_t zero = 0;
+    e = cudaMemcpyToSymbol(g_move_timeouts, &zero, sizeof zero);
+  }
+  *out = v;
+  return int(e);
 }
 
 int launch_xxh64(const HashUnit* units_dev, uint32_t n, const uint64_t* expect_dev, uint64_t* out_dev,

@@ -7,7 +7,7 @@
 namespace tsb {
 namespace dev {
 
-// ---- K1 / K4 / K5: batched copies ----
+// ---- K1 / K5: batched copies (and K4, the same batch HBM -> HBM) ----
 // One copy: `bytes` from src to dst; either side may be device memory, mapped pinned host memory or a peer GPU's
 // memory (P2P). A batch's copies must not overlap each other.
 struct Copy {
@@ -31,6 +31,12 @@ struct Batch {
   int32_t entry_val[kMaxEntries];
 };
 int launch_batch(const Batch& b, int blocks, void* stream);
+// K4: the same batch, HBM -> HBM only, staged through shared memory by TMA bulk copies (one warp per CTA, 192 KiB of
+// shared memory: one CTA per SM). Every copy 16-byte aligned with a 16-byte multiple size (move_fits), else
+// cudaErrorInvalidValue. move_take_timeouts: load waits that ran out since the last call, then reset (synchronous).
+bool move_fits(const Batch& b);
+int launch_move(const Batch& b, int blocks, void* stream);
+int move_take_timeouts(uint32_t* out);
 
 // ---- K3: device xxh64 of whole units ----
 // A unit is up to 4 spans hashed back to back (a gated unit's parts in the arena). out[i] = the hash; when expect is

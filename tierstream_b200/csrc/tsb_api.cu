@@ -42,11 +42,10 @@ void ck(cudaError_t e, const char* what) {
 
 }  // namespace
 
-extern "C" {
-
-ss_status tsb_land(const void* const* src, void* const* dst, const uint64_t* bytes, uint32_t n, int32_t* slot_of,
-                   const uint32_t* keys, const int32_t* vals, uint32_t n_entries, uint32_t* ready_word,
-                   uint32_t ready_val, uint32_t* counter, uint32_t blocks, void* stream) {
+namespace {
+ss_status land_or_move(bool move, const void* const* src, void* const* dst, const uint64_t* bytes, uint32_t n,
+                       int32_t* slot_of, const uint32_t* keys, const int32_t* vals, uint32_t n_entries,
+                       uint32_t* ready_word, uint32_t ready_val, uint32_t* counter, uint32_t blocks, void* stream) {
   return run([&] {
     tsb::require(n <= tsb::dev::kMaxCopies && n_entries <= tsb::dev::kMaxEntries, SS_E_INVALID,
                  "tsb_land: at most 384 copies and 128 entries per call");
@@ -70,9 +69,38 @@ ss_status tsb_land(const void* const* src, void* const* dst, const uint64_t* byt
       b->entry_key[i] = keys[i];
       b->entry_val[i] = vals[i];
     }
+    if (move) {
+      tsb::require(tsb::dev::move_fits(*b), SS_E_INVALID,
+                   "tsb_move: every address and size must be a multiple of 16 bytes (TMA bulk copies)");
+      const int grid = blocks ? int(blocks) : int(chunks < 1 ? 1 : chunks > 148 ? 148 : chunks);
+      ck(cudaError_t(tsb::dev::launch_move(*b, grid, stream)), "move kernel");
+      return;
+    }
     const int grid = blocks ? int(blocks) : int(chunks < 1 ? 1 : chunks > 296 ? 296 : chunks);
     ck(cudaError_t(tsb::dev::launch_batch(*b, grid, stream)), "land kernel");
   });
+}
+}  // namespace
+
+extern "C" {
+
+ss_status tsb_land(const void* const* src, void* const* dst, const uint64_t* bytes, uint32_t n, int32_t* slot_of,
+                   const uint32_t* keys, const int32_t* vals, uint32_t n_entries, uint32_t* ready_word,
+                   uint32_t ready_val, uint32_t* counter, uint32_t blocks, void* stream) {
+  return land_or_move(false, src, dst, bytes, n, slot_of, keys, vals, n_entries, ready_word, ready_val, counter,
+                      blocks, stream);
+}
+
+ss_status tsb_move(const void* const* src, void* const* dst, const uint64_t* bytes, uint32_t n, int32_t* slot_of,
+                   const uint32_t* keys, const int32_t* vals, uint32_t n_entries, uint32_t* ready_word,
+                   uint32_t ready_val, uint32_t* counter, uint32_t blocks, void* stream) {
+  return land_or_move(true, src, dst, bytes, n, slot_of, keys, vals, n_entries, ready_word, ready_val, counter,
+                      blocks, stream);
+}
+
+int tsb_move_timeouts(void) {
+  uint32_t v = 0;
+  return tsb::dev::move_take_timeouts(&v) == 0 ? int(v) : -1;
 }
 
 ss_status tsb_xxh64_units(const void* const* spans, const uint64_t* span_bytes, const uint32_t* n_spans, uint32_t n,

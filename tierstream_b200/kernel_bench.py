@@ -1,6 +1,6 @@
 """Per-kernel rates through the C ABI, each timed with CUDA events on the launching stream after warm-up, with inputs
-larger than L2: the land kernel (K1 / K4: one tsb_land launch per repetition) for pinned host -> HBM, HBM -> pinned
-host and HBM -> HBM, and the device xxh64 (K3: tsb_xxh64_units) for one unit alone (its serial chain) and for many
+larger than L2: the land kernel (K1: one tsb_land launch per repetition) for pinned host -> HBM, HBM -> pinned host
+and HBM -> HBM, the move kernel (K4: one tsb_move launch, HBM -> HBM, `--kernel move`), and the device xxh64 (K3: tsb_xxh64_units) for one unit alone (its serial chain) and for many
 units at once (aggregate). Also the small cases the committed ncu summaries were captured on.
 
     python -m tierstream_b200.kernel_bench land --dir h2d --part-bytes 33030144 --parts 15
@@ -30,8 +30,9 @@ def _events(stream, fn, reps, warmup):
     return times
 
 
-def land(direction, part_bytes, parts, reps, warmup):
-    """One tsb_land launch of `parts` copies of part_bytes each (at most 384), grid chosen by the library."""
+def land(direction, part_bytes, parts, reps, warmup, kernel="land"):
+    """One tsb_land launch (or tsb_move, HBM -> HBM through shared memory) of `parts` copies of part_bytes each (at
+    most 384), grid chosen by the library."""
     assert 1 <= parts <= 384
     total = part_bytes * parts
     dev = torch.empty(total, dtype=torch.uint8, device="cuda")
@@ -44,12 +45,17 @@ def land(direction, part_bytes, parts, reps, warmup):
     s = torch.cuda.Stream()
     lib = abi.load()
 
+    fn = lib.tsb_move if kernel == "move" else lib.tsb_land
+
     def once():
-        abi.check(lib.tsb_land(sp, dp, by, parts, None, None, None, 0, None, 0, None, 0, s.cuda_stream))
+        abi.check(fn(sp, dp, by, parts, None, None, None, 0, None, 0, None, 0, s.cuda_stream))
 
     t = _events(s, once, reps, warmup)
     ms = sorted(t)[len(t) // 2]
-    return {"kernel": "land", "dir": direction, "part_bytes": part_bytes, "parts": parts, "bytes": total,
+    if kernel == "move":
+        assert lib.tsb_move_timeouts() == 0
+        assert torch.equal(dst[:1 << 20], src[:1 << 20]) and torch.equal(dst[-(1 << 20):], src[-(1 << 20):])
+    return {"kernel": kernel, "dir": direction, "part_bytes": part_bytes, "parts": parts, "bytes": total,
             "ms_median": round(ms, 4), "gbs": round(total / ms / 1e6, 2),
             "hbm_traffic_gbs": round(total * (2 if direction == "d2d" else 1) / ms / 1e6, 2)}
 
@@ -92,6 +98,8 @@ def main():
     a1.add_argument("--dir", default="h2d", choices=["h2d", "d2h", "d2d"])
     a1.add_argument("--part-bytes", type=int, default=33030144)
     a1.add_argument("--parts", type=int, default=15)
+    a1.add_argument("--kernel", default="land", choices=["land", "move"],
+                    help="move: tsb_move (HBM -> HBM through shared memory by TMA bulk copies; --dir d2d only)")
     a2 = sub.add_parser("xxh64")
     a2.add_argument("--units", type=int, default=296)
     a2.add_argument("--part-bytes", type=int, default=12582912)
@@ -101,7 +109,8 @@ def main():
         p.add_argument("--warmup", type=int, default=3)
     a = ap.parse_args()
     if a.what == "land":
-        r = land(a.dir, a.part_bytes, a.parts, a.reps, a.warmup)
+        assert a.kernel == "land" or a.dir == "d2d", "the move kernel copies HBM -> HBM only"
+        r = land(a.dir, a.part_bytes, a.parts, a.reps, a.warmup, a.kernel)
     else:
         r = xxh64(a.units, a.part_bytes, a.n_parts, a.reps, a.warmup)
     print(json.dumps(r), flush=True)
