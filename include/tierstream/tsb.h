@@ -75,6 +75,13 @@ typedef struct tsb_dg_replay_config {
   uint32_t tokens, n_ids, n_pred;
   uint32_t move_bytes;
   uint32_t inclusive; /* dg_inclusive_blocks */
+  /* file tier (dg_disk_tier, synchronous reads): blocks = home_blocks + spare blocks; disk[keys] flags the plan's
+   * disk units; disk_staging staging buffers (block indices blocks ..); a file read copies the unit's bytes from
+   * src_units (keys x unit bytes) when given. xstats (optional): [tokens][6] disk_reads, disk_read_bytes,
+   * disk_stage_waits, disk_drops, disk_discards, file-homed units after each boundary. */
+  uint32_t disk_tier, disk_prefetch, home_blocks, disk_staging;
+  const uint8_t* disk;
+  uint64_t* xstats;
 } tsb_dg_replay_config;
 SS_API ss_status tsb_test_dg_replay(const tsb_dg_replay_config* cfg, const int32_t* ids, const int32_t* preds,
                                     int32_t* tables, uint64_t* stats, const uint8_t* src_units, uint64_t* read_sum);

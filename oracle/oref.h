@@ -25,7 +25,14 @@ typedef struct oref_dg_config {
   uint32_t move_bytes;          /* 1 = the transport moves real bytes (host arena and blocks); 2 = timing sample:
                                    real copies into 4 aliased unit buffers each for slots and blocks */
   uint32_t inclusive;           /* dg_inclusive_blocks (the clean-copy share) */
+  /* three-tier (dg_disk_tier, synchronous reads: disk_queue 1): blocks = home_blocks + spare blocks; disk[keys] = 1 for
+   * the plan's disk units; disk_staging staging buffers; a read copies src_units' bytes when given. xstats (optional):
+   * [tokens][OREF_NXSTATS] disk_reads, disk_read_bytes, disk_stage_waits, disk_drops, disk_discards, file units. */
+  uint32_t disk_tier, disk_prefetch, home_blocks, disk_staging;
+  const uint8_t* disk;
+  uint64_t* xstats;
 } oref_dg_config;
+#define OREF_NXSTATS 6
 
 /* Counters dumped per token (in this order). */
 #define OREF_NSTATS 16

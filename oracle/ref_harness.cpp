@@ -46,7 +46,7 @@ class HostTransport final : public ts::DgTransport {
     // move_bytes 2: a timing sample, every copy moves its real bytes but slots and blocks alias a ring of 4 unit
     // buffers each (the bytes read back through the table are then not meaningful)
     alias_slots_ = c.move_bytes == 2 ? 4 : slots;
-    alias_blocks_ = c.move_bytes == 2 ? 4 : c.blocks;
+    alias_blocks_ = c.move_bytes == 2 ? 4 : c.blocks + c.disk_staging;
     if (move_) {
       arena_.assign(size_t(alias_slots_) * unit_, 1);
       blocks_.assign(size_t(alias_blocks_) * unit_, 2);
@@ -70,6 +70,11 @@ class HostTransport final : public ts::DgTransport {
   void h2h(int32_t src, int32_t dst) override {
     if (move_) std::memmove(block_ptr(dst), block_ptr(src), unit_);
   }
+  // three-tier: the unit's bytes as its file holds them (synchronous, the transport's read_unit contract)
+  void read_unit(uint32_t key, int32_t block) override {
+    if (move_ && files_) pcopy(block_ptr(block), files_ + size_t(key) * unit_, unit_);
+  }
+  const uint8_t* files_ = nullptr;
   void d2h_part(Stream, int32_t slot, int32_t block, uint32_t p) override {
     if (!move_) return;
     uint64_t off = 0;
@@ -131,17 +136,26 @@ extern "C" __attribute__((visibility("default"))) int oref_dg_replay(const oref_
     cfg.wb_max_outstanding = c->wb_max_outstanding;
     cfg.max_ids = c->n_ids ? c->n_ids : 1;
     cfg.inclusive = c->inclusive;
+    cfg.disk_tier = c->disk_tier != 0;
+    cfg.disk_prefetch = c->disk_prefetch != 0;
+    cfg.home_blocks = c->home_blocks;
+    cfg.disk_staging = c->disk_staging;
+    cfg.disk_queue = 1;  // synchronous reads
     uint32_t keys = 0;
     for (uint32_t g = 0; g < c->n_gated; ++g) keys += c->n_units[g];
     const uint32_t slots = c->persistent_slots + 2 * c->bank_slots + 1;
     HostTransport t(*c, keys, slots);
+    t.files_ = src_units;
     ts::DgCore core(cfg, &t);
     std::vector<uint32_t> order(c->order, c->order + c->n_order);
     for (uint32_t k = 0; k < keys; ++k) order.push_back(k);
-    core.place(order);
+    std::vector<uint8_t> disk;
+    if (cfg.disk_tier && c->disk) disk.assign(c->disk, c->disk + keys);
+    core.place(order, disk.empty() ? nullptr : &disk);
     t.upload_table(core.table().data(), keys);
     if (t.move_ && src_units && c->move_bytes == 1)  // the open's fill: every unit into its slot or block
       for (uint32_t k = 0; k < keys; ++k) {
+        if (core.slot_of(k) < 0 && core.block_of(k) < 0) continue;  // (three-tier: a file home stays in its file)
         uint8_t* dst = core.slot_of(k) >= 0 ? t.slot_ptr(core.slot_of(k)) : t.block_ptr(core.block_of(k));
         std::memcpy(dst, src_units + size_t(k) * t.unit_, t.unit_);
       }
@@ -177,6 +191,11 @@ extern "C" __attribute__((visibility("default"))) int oref_dg_replay(const oref_
                                        s.bank_serves,     s.collected_mid, s.evicted,     s.evict_short,
                                        s.writebacks_done, s.wb_deferred, s.wb_cancelled,  s.wb_forced};
       std::memcpy(stats + size_t(tok) * OREF_NSTATS, v, sizeof v);
+      if (c->xstats) {
+        const uint64_t xv[OREF_NXSTATS] = {s.disk_reads, s.disk_read_bytes, s.disk_stage_waits, s.disk_drops,
+                                           s.disk_discards, core.file_units()};
+        std::memcpy(c->xstats + size_t(tok) * OREF_NXSTATS, xv, sizeof xv);
+      }
       core.check();
     }
     return 0;

@@ -129,7 +129,9 @@ class dg_replay_config(C.Structure):
                 ("prefetch_reserve", u32), ("prefetch_per_layer", u32), ("prefetch_per_token", u32),
                 ("wb_defer", u32), ("wb_on_d2h", u32), ("wb_layer_bytes", u64), ("wb_max_outstanding", u64),
                 ("n_order", u32), ("order", C.POINTER(u32)), ("tokens", u32), ("n_ids", u32), ("n_pred", u32),
-                ("move_bytes", u32), ("inclusive", u32)]
+                ("move_bytes", u32), ("inclusive", u32), ("disk_tier", u32), ("disk_prefetch", u32),
+                ("home_blocks", u32), ("disk_staging", u32), ("disk", C.POINTER(C.c_uint8)),
+                ("xstats", C.POINTER(u64))]
 
 
 class tsb_peer_tier(C.Structure):

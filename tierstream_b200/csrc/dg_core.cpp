@@ -22,6 +22,11 @@ SlotCache::SlotCache(const CacheConfig& cfg, Mover* m) : c_(cfg), m_(m) {
   bank_first_ = c_.persistent_slots;
   require(c_.inclusive == 0 || c_.inclusive < c_.blocks, SS_E_INVALID,
           "device-gated: the inclusive share must leave a block for write-backs");
+  require(!c_.disk_tier || c_.disk_staging >= 1, SS_E_INVALID, "device-gated: the file tier needs staging buffers");
+  require(c_.disk_tier || (!c_.disk_prefetch && !c_.disk_staging && !c_.home_blocks), SS_E_INVALID,
+          "device-gated: file tier options without the file tier");
+  require(uint64_t(c_.blocks) + c_.disk_staging < 0x7fffffffull, SS_E_INVALID, "device-gated: too many host blocks");
+  stage_ev_.assign(c_.disk_staging, nullptr);
   e_.assign(keys_, Entry{});
   table_.assign(keys_, -1);
   bank_key_.assign(2u * size_t(c_.bank_slots), kNil);
@@ -37,6 +42,10 @@ SlotCache::SlotCache(const CacheConfig& cfg, Mover* m) : c_(cfg), m_(m) {
 
 SlotCache::~SlotCache() {
   for (void* ev : all_events_) m_->event_destroy(ev);
+}
+
+void Mover::read_unit(uint32_t, int32_t) {
+  fail(SS_E_UNSUPPORTED, "device-gated: this mover cannot read a unit from its file");
 }
 
 [[noreturn]] void SlotCache::broken(const std::string& what) const {
@@ -67,7 +76,7 @@ void SlotCache::apply_wb_defer() {
   }
 }
 
-void SlotCache::place(const std::vector<uint32_t>& order) {
+void SlotCache::place(const std::vector<uint32_t>& order, const std::vector<uint8_t>* disk) {
   const uint32_t dev_max = c_.persistent_slots - c_.spare_target;
   std::vector<uint8_t> taken(keys_, 0);
   std::vector<uint32_t> dev;
@@ -78,14 +87,47 @@ void SlotCache::place(const std::vector<uint32_t>& order) {
       dev.push_back(k);
     }
   }
-  require(uint64_t(keys_) - dev.size() <= c_.blocks, SS_E_CAPACITY,
-          "device-gated: fewer host blocks than non-resident units");
+  // file tier: which non-resident keys get a block, as flags (the plan's pinned units first, then its disk units,
+  // each by priority: the order's keys first, then key order); host_rank is their recency order
+  const bool three = c_.disk_tier;
+  std::vector<uint8_t> blocked(keys_, 0);
+  std::vector<uint32_t> host_rank;
+  if (three) {
+    require(!disk || disk->size() == keys_, SS_E_INVALID, "device-gated: the disk flags do not cover the keys");
+    std::vector<uint8_t> seen(keys_, 0);
+    std::vector<uint32_t> prio;
+    for (uint32_t k : order)
+      if (!seen[k]) {
+        seen[k] = 1;
+        prio.push_back(k);
+      }
+    for (uint32_t k = 0; k < keys_; ++k)
+      if (!seen[k]) prio.push_back(k);
+    const uint32_t cap = std::min(c_.home_blocks, c_.blocks);
+    for (uint8_t pass = 0; pass < 2; ++pass)
+      for (uint32_t k : prio)
+        if (!taken[k] && (disk ? (*disk)[k] : uint8_t(0)) == pass && host_rank.size() < cap) {
+          blocked[k] = 1;
+          host_rank.push_back(k);
+        }
+  } else {
+    require(uint64_t(keys_) - dev.size() <= c_.blocks, SS_E_CAPACITY,
+            "device-gated: fewer host blocks than non-resident units");
+  }
   int32_t next_block = 0;
+  on_file_ = 0;
+  hhead_ = htail_ = kNil;
   for (uint32_t k = 0; k < keys_; ++k) {
     e_[k] = Entry{};
-    if (!taken[k]) e_[k].block = next_block++;  // Host home, blocks in key order
+    if (!taken[k] && (!three || blocked[k])) {
+      e_[k].block = next_block++;  // Host home, blocks in key order
+    } else if (!taken[k]) {
+      e_[k].home = Home::File;
+      ++on_file_;
+    }
     table_[k] = -1;
   }
+  for (size_t i = host_rank.size(); i-- > 0;) hpush(host_rank[i]);  // the first by priority most recently homed
   head_ = tail_ = kNil;
   for (uint32_t i = 0; i < dev.size(); ++i) {
     Entry& x = e_[dev[i]];
@@ -107,6 +149,83 @@ void SlotCache::place(const std::vector<uint32_t>& order) {
   open_head_ = head_;
   open_tail_ = tail_;
   open_on_device_ = on_device_;
+  open_hhead_ = hhead_;
+  open_htail_ = htail_;
+  open_on_file_ = on_file_;
+}
+
+// ---- file tier: the pinned homes' recency list (head = most recently homed; only kept with the file tier) ----
+void SlotCache::hpush(uint32_t k) {
+  if (!c_.disk_tier) return;
+  Entry& x = e_[k];
+  x.hprev = kNil;
+  x.hnext = hhead_;
+  if (hhead_ != kNil) e_[hhead_].hprev = k;
+  else htail_ = k;
+  hhead_ = k;
+  x.in_hlist = true;
+}
+
+void SlotCache::hunlink(uint32_t k) {
+  if (!c_.disk_tier) return;
+  Entry& x = e_[k];
+  if (!x.in_hlist) broken("a pinned home outside the pinned recency list");
+  if (x.hprev != kNil) e_[x.hprev].hnext = x.hnext;
+  else hhead_ = x.hnext;
+  if (x.hnext != kNil) e_[x.hnext].hprev = x.hprev;
+  else htail_ = x.hprev;
+  x.hprev = x.hnext = kNil;
+  x.in_hlist = false;
+}
+
+std::vector<uint32_t> SlotCache::host_order() const {
+  std::vector<uint32_t> out;
+  for (uint32_t k = hhead_; k != kNil; k = e_[k].hnext) out.push_back(k);
+  return out;
+}
+
+// A unit that leaves the device or a bank slot without a write-back: its block (a clean copy, or the block it was
+// served from) is its home again, else (file tier) its file.
+void SlotCache::to_lower(uint32_t k) {
+  Entry& x = e_[k];
+  x.slot = -1;
+  if (x.backed) {
+    x.backed = false;
+    --backed_;
+  }
+  if (x.block >= 0) {
+    x.home = Home::Host;
+    hpush(k);
+  } else {
+    if (!c_.disk_tier) broken("a unit without a block left the device without a write-back");
+    x.home = Home::File;
+    ++on_file_;
+  }
+}
+
+// The least recently homed pinned unit goes to its file (no copy: the file holds its bytes); its block is free.
+bool SlotCache::drop_host_lru() {
+  if (!c_.disk_tier || htail_ == kNil) return false;
+  const uint32_t k = htail_;
+  Entry& x = e_[k];
+  hunlink(k);
+  free_blocks_.push_back(x.block);
+  x.block = -1;
+  x.home = Home::File;
+  ++on_file_;
+  ++st_.disk_drops;
+  return true;
+}
+
+// The next staging buffer in rotation, once its last copy landed.
+int32_t SlotCache::take_stage() {
+  const uint32_t i = stage_next_;
+  stage_next_ = (i + 1) % c_.disk_staging;
+  if (stage_ev_[i] && !m_->done(stage_ev_[i])) {
+    m_->event_sync(stage_ev_[i]);
+    ++st_.disk_stage_waits;
+  }
+  return int32_t(c_.blocks + i);
 }
 
 // ---- the recency list (head = most recently used) ----
@@ -147,17 +266,6 @@ void SlotCache::publish(Mover::Stream s, uint32_t k, int32_t v) {
   m_->publish(s, k, v);
 }
 
-void SlotCache::to_host(uint32_t k) {
-  Entry& x = e_[k];
-  if (x.block < 0) broken("a unit without a block left the device without a write-back");
-  x.slot = -1;
-  x.home = Home::Host;
-  if (x.backed) {
-    x.backed = false;
-    --backed_;
-  }
-}
-
 // Finished write-backs in submission order: the unit's home becomes its block and its slot is free; a discarded one
 // (the unit was resurrected) only returns its block.
 uint32_t SlotCache::collect() {
@@ -173,6 +281,7 @@ uint32_t SlotCache::collect() {
       x.home = Home::Host;
       x.block = w.block;
       x.slot = -1;
+      hpush(w.key);
       free_slots_.push_back(w.slot);
     }
     ++n;
@@ -267,7 +376,7 @@ int32_t SlotCache::bank_slot(uint32_t g) {
   const int32_t slot = int32_t(bank_first_ + idx);
   const uint32_t old = bank_key_[idx];
   if (old != kNil && e_[old].home == Home::Bank && e_[old].slot == slot) {
-    to_host(old);
+    to_lower(old);  // its block, or (read from it) its file
     publish(Mover::kDem, old, -1);
   }
   bank_key_[idx] = kNil;
@@ -330,15 +439,19 @@ bool SlotCache::fetch(uint32_t g, uint32_t unit, bool prefetch) {
     }
     case Home::Host:
       break;
+    case Home::File:  // a file read below; a prefetch only with disk_prefetch
+      if (prefetch && !c_.disk_prefetch) return false;
+      break;
   }
   const size_t reserve = prefetch ? c_.prefetch_reserve : 0u;
   if (free_slots_.size() <= reserve || (pressure_ && !prefetch)) st_.collected_mid += collect();
   const bool capped = !prefetch && pressure_ && demand_free_used_ >= pressure_free_;
   if (!prefetch && !capped && free_slots_.empty()) force_free_slot();
   int32_t slot = -1;
-  bool bank = false;
+  bool bank = false, free_counted = false;
   if (!capped && free_slots_.size() > reserve) {
     if (!prefetch) ++demand_free_used_;
+    free_counted = !prefetch;
     slot = free_slots_.back();
     free_slots_.pop_back();
   } else if (prefetch) {
@@ -360,12 +473,40 @@ bool SlotCache::fetch(uint32_t g, uint32_t unit, bool prefetch) {
     }
   }
   const Mover::Stream s = prefetch ? Mover::kPf : Mover::kDem;
+  const bool from_file = x.home == Home::File;
+  int32_t src = x.block;
+  if (from_file) {  // its bytes from the file into a staging buffer, then the same copy
+    const int32_t stage = take_stage();
+    const auto t0 = std::chrono::steady_clock::now();
+    try {
+      m_->read_unit(k, stage);
+    } catch (...) {  // nothing enqueued for this key: its slot goes back (a bank slot stays used, unpublished)
+      if (!bank) {
+        free_slots_.push_back(slot);
+        if (free_counted) --demand_free_used_;
+      }
+      throw;
+    }
+    st_.disk_read_ns += uint64_t(
+        std::chrono::duration_cast<std::chrono::nanoseconds>(std::chrono::steady_clock::now() - t0).count());
+    ++st_.disk_reads;
+    st_.disk_read_bytes += unit_bytes_;
+    src = stage;
+  }
   if (mut_ == kEntryBeforeCopy) {  // test-only fault: the entry before its bytes
     publish(s, k, slot);
-    m_->h2d(s, slot, x.block, k);
+    m_->h2d(s, slot, src, k);
   } else {
-    m_->h2d(s, slot, x.block, k);
+    m_->h2d(s, slot, src, k);
     publish(s, k, slot);
+  }
+  if (from_file) {  // the staging buffer is reusable once this copy landed
+    void*& ev = stage_ev_[uint32_t(src) - c_.blocks];
+    if (!ev) ev = event();
+    m_->record(ev, s);
+    --on_file_;
+  } else {
+    hunlink(k);  // (a Host unit: out of the pinned recency list)
   }
   x.slot = slot;
   x.via_pf = prefetch;
@@ -508,7 +649,7 @@ void SlotCache::end_token(const std::vector<uint32_t>& keep) {
       pool_.push_back(x.pf_done);
       x.pf_done = nullptr;
     }
-    if (x.block >= 0) {
+    if (x.block >= 0) {  // (a unit read from its file holds none)
       if (backed_ < c_.inclusive) {  // inclusive share: the source block stays as a clean copy of the slot's bytes
         x.backed = true;
         ++backed_;
@@ -520,10 +661,10 @@ void SlotCache::end_token(const std::vector<uint32_t>& keep) {
     }
   }
   coming_.clear();
-  for (uint32_t k : banked_) {  // bank units go back to their blocks
+  for (uint32_t k : banked_) {  // bank units go back to their blocks (or, read from it, their file)
     Entry& x = e_[k];
     if (x.home == Home::Bank) {
-      to_host(k);
+      to_lower(k);
       table_[k] = -1;
     }
     if (x.pf_done) {
@@ -549,12 +690,15 @@ void SlotCache::end_token(const std::vector<uint32_t>& keep) {
   };
   auto accept = [&](uint32_t k) {
     Entry& x = e_[k];
-    if (x.backed) {  // a clean copy: its block is its home again, no write-back
-      ++st_.inclusive_drops;
+    // a clean copy (its block is its home again) or, file tier with no block to free, its file: no copy; a pinned
+    // unit dropped to its file frees a block first when none is free
+    if (x.backed || (free_blocks_.empty() && !drop_host_lru() && c_.disk_tier)) {
+      if (x.backed) ++st_.inclusive_drops;
+      else ++st_.disk_discards;
       unlink(k);
       --on_device_;
       free_slots_.push_back(x.slot);
-      to_host(k);
+      to_lower(k);
       table_[k] = -1;
       ++st_.evicted;
       ++lc_[gated_of(k)].evicted;
@@ -637,6 +781,7 @@ uint32_t SlotCache::seed(const std::vector<uint32_t>& keys) {
     const int32_t slot = free_slots_.back();
     free_slots_.pop_back();
     m_->h2d(Mover::kDem, slot, x.block, k);
+    hunlink(k);
     free_blocks_.push_back(x.block);
     x.block = -1;
     x.slot = slot;
@@ -692,9 +837,11 @@ void SlotCache::set_pressure(uint32_t free_per_token, uint32_t evict_recent) {
   pressure_recent_ = evict_recent;
 }
 
-// Locations: slots [0, P), blocks [P, P + blocks), and the reset staging buffer. Every misplaced unit moves once:
-// chains that end in a free location first (each move fills the hole the previous one left), then the remaining
-// cycles through the staging buffer. The mover executes each move before the next one reads its destination.
+// Locations: slots [0, P), blocks [P, P + blocks), the reset staging buffer and (file tier) the unit's file. Every
+// misplaced unit moves once: units going back to their file first (no copy, their location vacated), then chains
+// that end in a free location (each move fills the hole the previous one left; a unit read from its file ends its
+// chain), then the remaining cycles through the staging buffer (dg_core.cpp:2976-3075). The mover executes each move
+// before the next one reads its destination.
 void SlotCache::reset_open() {
   require(open_e_.size() == keys_, SS_E_INVALID, "device-gated: reset before place");
   drain();
@@ -707,19 +854,29 @@ void SlotCache::reset_open() {
       pool_.push_back(x.pf_done);
       x.pf_done = nullptr;
     }
-  const size_t P = c_.persistent_slots, N = P + c_.blocks, stage = N;
+  for (void* ev : stage_ev_)  // every staging copy landed
+    if (ev) m_->event_sync(ev);
+  const size_t P = c_.persistent_slots, N = P + c_.blocks, stage = N, file = N + 1;
   std::vector<size_t> cur(keys_), dst(keys_);
   std::vector<uint32_t> occupant(N + 1, kNil), wanted(N + 1, kNil);
   for (uint32_t k = 0; k < keys_; ++k) {
     const Entry& x = e_[k];
     if (x.home == Home::Evicting) broken("reset left an evicting unit");
+    // a unit read from its file has no block: a Coming one's slot is its only copy; a bank slot is no persistent
+    // location, so a bank unit read from its file goes back to it
     const bool on_slot = x.home == Home::Device || (x.home == Home::Coming && x.block < 0);
-    cur[k] = on_slot ? size_t(x.slot) : P + size_t(x.block);
+    const bool in_file = x.home == Home::File || (x.home == Home::Bank && x.block < 0);
+    cur[k] = in_file ? file : on_slot ? size_t(x.slot) : P + size_t(x.block);
     const Entry& o = open_e_[k];
-    dst[k] = o.home == Home::Device ? size_t(o.slot) : P + size_t(o.block);
-    occupant[cur[k]] = k;
-    wanted[dst[k]] = k;
+    dst[k] = o.home == Home::File ? file : o.home == Home::Device ? size_t(o.slot) : P + size_t(o.block);
+    if (cur[k] != file) occupant[cur[k]] = k;
+    if (dst[k] != file) wanted[dst[k]] = k;
   }
+  for (uint32_t k = 0; k < keys_; ++k)  // back to its file: its location is vacated, no copy
+    if (dst[k] == file && cur[k] != file) {
+      occupant[cur[k]] = kNil;
+      cur[k] = file;
+    }
   // plan every move first (bookkeeping only), then execute them in order; consecutive slot-to-slot moves share
   // launches: a move's wave is one after every earlier move that reads its destination or writes its source
   struct Move {
@@ -731,7 +888,7 @@ void SlotCache::reset_open() {
     const size_t from = cur[k];
     if (to > N || occupant[to] != kNil) broken("reset would overwrite a live source");
     plan.push_back({from, to, k});
-    occupant[from] = kNil;
+    if (from != file) occupant[from] = kNil;
     occupant[to] = k;
     cur[k] = to;
   };
@@ -746,6 +903,7 @@ void SlotCache::reset_open() {
   }
   for (uint32_t k = 0; k < keys_; ++k) {
     if (cur[k] == dst[k]) continue;
+    if (cur[k] == file) broken("reset left a file read behind");
     size_t hole = cur[k];
     move(k, stage);
     while (hole != dst[k]) {
@@ -778,7 +936,13 @@ void SlotCache::reset_open() {
       continue;
     }
     flush_d2d();
-    if (mv.from < P) {
+    if (mv.from == file && mv.to < P) {  // read into the reset staging buffer, then to the slot
+      m_->read_unit(mv.key, -1);
+      m_->h2d(Mover::kDem, int32_t(mv.to), -1, mv.key);
+      m_->sync(Mover::kDem);
+    } else if (mv.from == file) {
+      m_->read_unit(mv.key, blk(mv.to));
+    } else if (mv.from < P) {
       m_->d2h(Mover::kD2h, int32_t(mv.from), blk(mv.to), -1, mv.key);
       m_->sync(Mover::kD2h);
     } else if (mv.to < P) {
@@ -799,6 +963,10 @@ void SlotCache::reset_open() {
   head_ = open_head_;
   tail_ = open_tail_;
   on_device_ = open_on_device_;
+  hhead_ = open_hhead_;
+  htail_ = open_htail_;
+  on_file_ = open_on_file_;
+  stage_next_ = 0;
   coming_.clear();
   banked_.clear();
   std::fill(bank_key_.begin(), bank_key_.end(), kNil);
@@ -824,11 +992,15 @@ void SlotCache::check() const {
     if (i < 0 || size_t(i) >= v.size() || v[size_t(i)]) broken(what);
     v[size_t(i)] = 1;
   };
-  uint32_t listed = 0, dev = 0;
+  uint32_t listed = 0, dev = 0, hlisted = 0, hosts = 0, files = 0;
   for (uint32_t k = head_; k != kNil; k = e_[k].next) {
     if (++listed > keys_) broken("the recency list has a cycle");
     const Home h = e_[k].home;
     if (h != Home::Device && h != Home::Coming) broken("a listed unit is not on the device");
+  }
+  for (uint32_t k = hhead_; k != kNil; k = e_[k].hnext) {
+    if (++hlisted > keys_) broken("the pinned recency list has a cycle");
+    if (e_[k].home != Home::Host || !e_[k].in_hlist) broken("a unit in the pinned recency list is not a pinned home");
   }
   for (uint32_t k = 0; k < keys_; ++k) {
     const Entry& x = e_[k];
@@ -837,6 +1009,13 @@ void SlotCache::check() const {
         take(block_used, x.block, "a host unit without its own block");
         if (table_[k] != -1) broken("a host unit with a published entry");
         if (x.listed) broken("a host unit in the recency list");
+        ++hosts;
+        break;
+      case Home::File:
+        if (!c_.disk_tier) broken("a file home without the file tier");
+        if (x.slot >= 0 || x.block >= 0 || x.listed || x.in_hlist) broken("a file home holding a slot or a block");
+        if (table_[k] != -1) broken("a file home with a published entry");
+        ++files;
         break;
       case Home::Device:
       case Home::Coming:
@@ -845,14 +1024,16 @@ void SlotCache::check() const {
         if (x.slot >= int32_t(c_.persistent_slots)) broken("a device unit in a bank slot");
         if (table_[k] != x.slot) broken("a device unit's entry is not its slot");
         if (!x.listed) broken("a device unit outside the recency list");
-        if (x.home == Home::Coming) take(block_used, x.block, "a coming unit without its source block");
-        else if (x.backed) take(block_used, x.block, "a clean copy without its own block");
+        if (x.home == Home::Coming && (x.block >= 0 || !c_.disk_tier))
+          take(block_used, x.block, "a coming unit without its source block");
+        else if (x.home == Home::Coming) {  // (read from its file)
+        } else if (x.backed) take(block_used, x.block, "a clean copy without its own block");
         else if (x.block >= 0) broken("a device unit still holding a block");
         if (x.backed && x.home != Home::Device) broken("a clean copy of a unit not on the device");
         break;
       case Home::Bank:
         take(slot_used, x.slot, "a bank unit without its own slot");
-        take(block_used, x.block, "a bank unit without its block");
+        if (x.block >= 0 || !c_.disk_tier) take(block_used, x.block, "a bank unit without its block");
         if (x.slot < int32_t(c_.persistent_slots)) broken("a bank unit in a persistent slot");
         if (table_[k] != x.slot) broken("a bank unit's entry is not its slot");
         break;
@@ -864,6 +1045,8 @@ void SlotCache::check() const {
     }
   }
   if (dev != on_device_ || dev != listed) broken("the device count disagrees with the homes");
+  if (files != on_file_) broken("the file count disagrees with the homes");
+  if (c_.disk_tier && hosts != hlisted) broken("the pinned recency list does not hold every pinned home");
   for (int32_t s : free_slots_) take(slot_used, s, "a free slot that is also in use");
   for (int32_t b : free_blocks_) take(block_used, b, "a free block that is also in use");
   for (const Writeback& w : wbs_)

@@ -4,12 +4,14 @@
 //
 // Every gated unit (key = unit_base[g] + unit) has one home: a slot of the arena shared by all gated layers
 // (Device; Coming while its copy is in flight; Bank for a demand served through a per-layer bank slot; Evicting while
-// its write-back runs) or a pinned block (Host). Inside a token entries only go from -1 to a slot, published on the
-// stream that copied the bytes; evictions happen at the boundary (end_token), whose write-backs are either enqueued
-// there or deferred part by part into the next token's served layers.
+// its write-back runs), a pinned block (Host), or, with the file tier, only its file (File). Inside a token entries
+// only go from -1 to a slot, published on the stream that copied the bytes; evictions happen at the boundary
+// (end_token), whose write-backs are either enqueued there or deferred part by part into the next token's served
+// layers.
 //
-// The decisions are those of the reference's DgCore (dg_core.cpp) for its two-tier LRU configuration, so the slot
-// table after every token matches it on the same trace when the schedule is deterministic:
+// The decisions are those of the reference's DgCore (dg_core.cpp) for its LRU configuration with two tiers, or three
+// with synchronous file reads, so the slot table after every token matches it on the same trace when the schedule is
+// deterministic:
 //   - open placement: residents by priority into slots 0.., every other key a block in key order
 //     (dg_core.cpp:769-858); free slots and blocks are LIFO stacks whose next is the lowest index;
 //   - a demand miss takes the last free slot, else (write-backs deferred) waits for one, else its layer's bank slot
@@ -17,7 +19,13 @@
 //   - a prefetch keeps prefetch_reserve slots free and stays under the per-layer and per-token budgets;
 //   - the boundary admits the token's arrivals, returns bank units to their blocks, collects finished write-backs,
 //     then evicts from the recency tail until free + pending write-backs reaches the spare target, one free block per
-//     victim (dg_core.cpp:1636-1927); deferred write-backs are carried and flushed by the same counts.
+//     victim (dg_core.cpp:1636-1927); deferred write-backs are carried and flushed by the same counts;
+//   - file tier (the reference's dg_disk_tier with synchronous reads, dg_disk_queue 0 / 1): the open gives blocks to
+//     home_blocks non-resident units (the plan's pinned units first, then by priority) and leaves the rest in their
+//     files; a file miss reads the unit into the next of disk_staging staging buffers (round robin, after that
+//     buffer's last copy landed) and copies it from there; pinned homes keep a recency order of their own, and a
+//     victim with no free block frees one by dropping the least recently homed pinned unit to its file, or goes to
+//     its own file when no pinned unit is left (dg_core.cpp:113-238, 769-858, 1146-1368, 1783).
 #pragma once
 
 #include <cstdint>
@@ -43,6 +51,9 @@ class Mover {
   // ascending order. Complete when the call returns.
   virtual void d2d_moves(const std::vector<std::pair<int32_t, int32_t>>& moves, const std::vector<uint32_t>& wave) = 0;
   virtual void h2h(int32_t src_block, int32_t dst_block, uint32_t key) = 0;
+  // File tier: every part of unit `key` from its file into `block` (blocks [blocks, blocks + disk_staging) are the
+  // staging buffers, -1 the reset staging buffer), synchronously; no copy reads the block meanwhile.
+  virtual void read_unit(uint32_t key, int32_t block);
   // slot_of[key] = v after everything enqueued on s so far (a release at system scope).
   virtual void publish(Stream s, uint32_t key, int32_t v) = 0;
   // ready[g] = seq on kDem after everything enqueued there.
@@ -76,6 +87,9 @@ struct CacheConfig {
   // Inclusive share (dg_inclusive_blocks): at most this many device units keep the pinned block they were promoted
   // from as a clean copy, so their eviction is a drop with no write-back (0 = exclusive).
   uint32_t inclusive = 0;
+  // File tier (dg_disk_tier): see the file comment. disk_prefetch: predictions may read file-homed units too.
+  bool disk_tier = false, disk_prefetch = false;
+  uint32_t home_blocks = 0, disk_staging = 0;
 };
 
 struct CacheStats {
@@ -87,6 +101,10 @@ struct CacheStats {
   uint64_t wb_forced_wait_ns = 0;
   uint64_t reset_moves = 0, reset_bytes = 0;
   uint64_t inclusive_kept = 0, inclusive_drops = 0;
+  // file tier: reads of file-homed units and their bytes and summed time; reads that waited for their staging
+  // buffer's last copy; pinned units dropped to their file to free a block; victims dropped to their file
+  uint64_t disk_reads = 0, disk_read_bytes = 0, disk_read_ns = 0, disk_stage_waits = 0, disk_drops = 0;
+  uint64_t disk_discards = 0;
 };
 
 struct LayerCounts {
@@ -95,7 +113,7 @@ struct LayerCounts {
 
 class SlotCache {
  public:
-  enum class Home : uint8_t { Host, Device, Coming, Bank, Evicting };
+  enum class Home : uint8_t { Host, Device, Coming, Bank, Evicting, File };
   enum Mutation { kNone0 = 0, kEntryBeforeCopy = 1, kNoCover = 2 };
 
   SlotCache(const CacheConfig& cfg, Mover* m);
@@ -104,8 +122,10 @@ class SlotCache {
   SlotCache& operator=(const SlotCache&) = delete;
 
   // Open: `order` names keys by priority (duplicates ignored); the first persistent_slots - spare_target distinct
-  // ones take slots 0.., in that recency order; every other key takes a block, numbered in key order.
-  void place(const std::vector<uint32_t>& order);
+  // ones take slots 0.., in that recency order; every other key takes a block, numbered in key order. File tier:
+  // `disk` flags the plan's disk units; only min(home_blocks, blocks) non-resident keys take a block (unflagged ones
+  // first, each group by priority; the first most recently homed), the others are file-homed.
+  void place(const std::vector<uint32_t>& order, const std::vector<uint8_t>* disk = nullptr);
 
   uint32_t keys() const { return keys_; }
   uint32_t gated() const { return uint32_t(base_.size() - 1); }
@@ -122,6 +142,9 @@ class SlotCache {
   uint32_t free_blocks() const { return uint32_t(free_blocks_.size()); }
   uint32_t deferred() const { return uint32_t(deferred_.size()); }
   uint32_t backed_units() const { return backed_; }
+  uint32_t file_units() const { return on_file_; }
+  // Pinned homes, most recently homed first (file tier only).
+  std::vector<uint32_t> host_order() const;
   uint64_t wb_outstanding_bytes() const { return outstanding_; }
   const CacheStats& stats() const { return st_; }
   const std::vector<LayerCounts>& layer_counts() const { return lc_; }
@@ -162,6 +185,8 @@ class SlotCache {
     uint32_t prev = kNil, next = kNil;
     bool listed = false, wb_pending = false, via_pf = false, used = false;
     bool backed = false;  // a device unit whose block still holds its bytes (inclusive share)
+    bool in_hlist = false;           // file tier: in the pinned homes' recency list
+    uint32_t hprev = kNil, hnext = kNil;
     void* pf_done = nullptr;
   };
   struct Writeback {
@@ -187,7 +212,11 @@ class SlotCache {
   void* finish_front();
   void force_free_slot();
   int32_t bank_slot(uint32_t g);
-  void to_host(uint32_t k);
+  void to_lower(uint32_t k);
+  void hpush(uint32_t k);
+  void hunlink(uint32_t k);
+  bool drop_host_lru();
+  int32_t take_stage();
   void publish(Mover::Stream s, uint32_t k, int32_t v);
   bool fetch(uint32_t g, uint32_t unit, bool prefetch);
   void cover(uint32_t g, uint32_t unit);
@@ -204,6 +233,9 @@ class SlotCache {
   std::vector<int32_t> free_slots_, free_blocks_, open_free_slots_, open_free_blocks_;
   uint32_t head_ = kNil, tail_ = kNil, on_device_ = 0, backed_ = 0;
   uint32_t open_head_ = kNil, open_tail_ = kNil, open_on_device_ = 0;
+  uint32_t hhead_ = kNil, htail_ = kNil, on_file_ = 0, open_hhead_ = kNil, open_htail_ = kNil, open_on_file_ = 0;
+  uint32_t stage_next_ = 0;
+  std::vector<void*> stage_ev_;  // per staging buffer: its last copy's event
   std::deque<Writeback> wbs_;
   std::deque<Deferred> deferred_;
   Mover::Stream wb_stream_ = Mover::kDem;

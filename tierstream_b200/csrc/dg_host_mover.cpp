@@ -14,8 +14,9 @@ namespace {
 
 class HostMover final : public Mover {
  public:
-  HostMover(const std::vector<uint64_t>& parts, uint32_t keys, uint32_t slots, uint32_t blocks, bool move)
-      : parts_(parts), table_(keys, -1), move_(move) {
+  HostMover(const std::vector<uint64_t>& parts, uint32_t keys, uint32_t slots, uint32_t blocks, bool move,
+            const uint8_t* files)
+      : parts_(parts), table_(keys, -1), move_(move), files_(files) {
     for (uint64_t b : parts_) unit_ += b;
     if (move_) {
       arena_.assign(size_t(slots) * unit_, 0);
@@ -48,6 +49,9 @@ class HostMover final : public Mover {
   void h2h(int32_t src, int32_t dst, uint32_t) override {
     if (move_) std::memmove(block_ptr(dst), block_ptr(src), unit_);
   }
+  void read_unit(uint32_t key, int32_t block) override {
+    if (move_ && files_) std::memcpy(block_ptr(block), files_ + size_t(key) * unit_, unit_);
+  }
   void publish(Stream, uint32_t key, int32_t v) override { table_[key] = v; }
   void ready(uint32_t, uint32_t) override {}
   void* event_create() override { return new int(0); }
@@ -64,6 +68,7 @@ class HostMover final : public Mover {
   std::vector<uint8_t> arena_, blocks_, stage_;
   uint64_t unit_ = 0;
   bool move_;
+  const uint8_t* files_;  // each unit's bytes as its file holds them (file tier)
 };
 
 uint64_t checksum(const uint8_t* p, uint64_t n) {
@@ -93,17 +98,24 @@ void dg_replay(const tsb_dg_replay_config* c, const int32_t* ids, const int32_t*
   cfg.wb_layer_bytes = c->wb_layer_bytes;
   cfg.wb_max_outstanding = c->wb_max_outstanding;
   cfg.inclusive = c->inclusive;
+  cfg.disk_tier = c->disk_tier != 0;
+  cfg.disk_prefetch = c->disk_prefetch != 0;
+  cfg.home_blocks = c->home_blocks;
+  cfg.disk_staging = c->disk_staging;
   uint32_t keys = 0;
   for (uint32_t g = 0; g < c->n_gated; ++g) keys += c->n_units[g];
   HostMover m(std::vector<uint64_t>(c->part_bytes, c->part_bytes + c->n_parts), keys,
-              c->persistent_slots + 2 * c->bank_slots + 1, c->blocks, c->move_bytes != 0);
+              c->persistent_slots + 2 * c->bank_slots + 1, c->blocks + c->disk_staging, c->move_bytes != 0, src_units);
   SlotCache core(cfg, &m);
   std::vector<uint32_t> order(c->order, c->order + c->n_order);
   for (uint32_t k = 0; k < keys; ++k) order.push_back(k);
-  core.place(order);
+  std::vector<uint8_t> disk;
+  if (cfg.disk_tier && c->disk) disk.assign(c->disk, c->disk + keys);
+  core.place(order, disk.empty() ? nullptr : &disk);
   m.upload_table(core.table().data(), keys);
-  if (m.move_ && src_units)
+  if (m.move_ && src_units)  // the open's fill: every unit with a slot or a block (a file home stays in its file)
     for (uint32_t k = 0; k < keys; ++k) {
+      if (core.slot_of(k) < 0 && core.block_of(k) < 0) continue;
       uint8_t* dst = core.slot_of(k) >= 0 ? m.slot_ptr(core.slot_of(k)) : m.block_ptr(core.block_of(k));
       std::memcpy(dst, src_units + size_t(k) * m.unit_, m.unit_);
     }
@@ -139,6 +151,11 @@ void dg_replay(const tsb_dg_replay_config* c, const int32_t* ids, const int32_t*
                             s.evicted,       s.evict_short, s.writebacks_done, s.wb_deferred, s.wb_cancelled,
                             s.wb_forced};
     std::memcpy(stats + size_t(t) * 16, v, sizeof v);
+    if (c->xstats) {
+      const uint64_t xv[6] = {s.disk_reads, s.disk_read_bytes, s.disk_stage_waits, s.disk_drops, s.disk_discards,
+                              core.file_units()};
+      std::memcpy(c->xstats + size_t(t) * 6, xv, sizeof xv);
+    }
     core.check();
   }
 }

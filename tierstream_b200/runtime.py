@@ -240,8 +240,10 @@ class TokenGraph:
 
 def replay_config(n_units, part_bytes, persistent_slots, bank_slots, blocks, spare_target, order, tokens, n_ids,
                   n_pred=0, prefetch_reserve=0xFFFFFFFF, prefetch_per_layer=4, prefetch_per_token=48, wb_defer=1,
-                  wb_on_d2h=1, wb_layer_bytes=0, wb_max_outstanding=0, move_bytes=0, inclusive=0):
-    """A dg_replay_config with its arrays kept alive on the returned object."""
+                  wb_on_d2h=1, wb_layer_bytes=0, wb_max_outstanding=0, move_bytes=0, inclusive=0, disk=None,
+                  home_blocks=0, disk_staging=0, disk_prefetch=0):
+    """A dg_replay_config with its arrays kept alive on the returned object. disk (file tier): one flag per key for
+    the plan's disk units (blocks then counts home_blocks + the spare blocks); xstats is attached by replay()."""
     c = abi.dg_replay_config()
     keep = {}
     keep["n_units"] = (C.c_uint32 * len(n_units))(*n_units)
@@ -259,13 +261,19 @@ def replay_config(n_units, part_bytes, persistent_slots, bank_slots, blocks, spa
     c.n_order = len(order)
     c.order = keep["order"]
     c.tokens, c.n_ids, c.n_pred, c.move_bytes, c.inclusive = tokens, n_ids, n_pred, move_bytes, inclusive
+    if disk is not None:
+        keep["disk"] = (C.c_uint8 * max(1, len(disk)))(*[1 if f else 0 for f in disk])
+        c.disk_tier, c.disk_prefetch, c.home_blocks, c.disk_staging = 1, disk_prefetch, home_blocks, disk_staging
+        c.disk = keep["disk"]
     c._keep = keep
     return c
 
 
-def replay(cfg, ids, preds=None, src_units=None, want_reads=False):
-    """This library's deterministic replay (tsb_test_dg_replay): (tables, stats[, read_sum])."""
+def replay(cfg, ids, preds=None, src_units=None, want_reads=False, xstats=None):
+    """This library's deterministic replay (tsb_test_dg_replay): (tables, stats[, read_sum]). xstats: an optional
+    uint64 array [tokens][6] filled with the file tier's counters after each boundary."""
     keys = sum(cfg.n_units[i] for i in range(cfg.n_gated))
+    cfg.xstats = xstats.ctypes.data_as(C.POINTER(C.c_uint64)) if xstats is not None else None
     ids = np.ascontiguousarray(ids, dtype=np.int32)
     tables = np.empty((cfg.tokens, keys), dtype=np.int32)
     stats = np.empty((cfg.tokens, 16), dtype=np.uint64)
