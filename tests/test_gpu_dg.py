@@ -190,3 +190,101 @@ def test_predictions_tables_match_reference(small_model, orc, ref, monkeypatch, 
         assert st["prefetched"] == s_ref[-1][5] and st["prefetched"] > 0
     finally:
         run.close()
+
+
+def file_tier_run(m, R=3, pinned=4, S=3, **kw):
+    """A DgRun with the file tier: per layer units [0, R) resident, [R, R + pinned) pinned, the rest in the model file
+    only (tier DISK)."""
+    res = [g * m.units + u for g in range(m.layers) for u in range(R)]
+    disk = [g * m.units + u for g in range(m.layers) for u in range(R + pinned, m.units)]
+    run = harness.DgRun(m, resident_keys=res, max_ids=2, disk_keys=disk, disk_staging=S, **kw)
+    return run, res, disk
+
+
+def file_tier_cfg(run, m, res, disk, ids, S, **kw):
+    flags = [0] * (m.layers * m.units)
+    for k in disk:
+        flags[k] = 1
+    P = m.layers * m.units - len(res) - len(disk)
+    return runtime.replay_config([m.units] * m.layers, list(m.part_bytes), persistent_slots=len(res) + m.layers,
+                                 bank_slots=run.n_ids, blocks=P + m.layers, spare_target=m.layers, order=res,
+                                 tokens=ids.shape[0], n_ids=run.n_ids, disk=flags, home_blocks=P, disk_staging=S,
+                                 **kw)
+
+
+@pytest.mark.parametrize("wb_defer", [0, 1])
+def test_file_tier_bytes_and_tables_match_reference(small_model, orc, ref, monkeypatch, wb_defer):
+    """The file tier (dg_disk_tier, synchronous reads): units of tier DISK are read from the model file into a pinned
+    staging buffer on their miss and copied from there; every routed unit's bytes are the source's, and the slot table
+    and the file tier's counters after every token equal the reference DgCore's replay."""
+    monkeypatch.setenv("TSB_DG_DETERMINISTIC", "1")
+    m = small_model
+    ids = synth.zipf_trace(40, m.layers, m.units, 2, s=0.8, seed=21)
+    run, res, disk = file_tier_run(m, S=3, verify=True, wb_defer=wb_defer)
+    try:
+        cfg = file_tier_cfg(run, m, res, disk, ids, 3, wb_defer=wb_defer)
+        x_ref = np.zeros((ids.shape[0], 6), dtype=np.uint64)
+        t_ref, s_ref = oracle.ref_replay(cfg, ids, xstats=x_ref)
+        want = expected_sums(m, orc)
+        for t in range(ids.shape[0]):
+            got = run.step(ids[t])
+            keys = np.arange(m.layers)[:, None] * m.units + ids[t]
+            assert np.array_equal(got, want[keys]), "token %d read wrong bytes" % t
+            assert np.array_equal(run.ctx.table(run.keys), t_ref[t]), "slot table differs after token %d" % t
+        st = run.ctx.stats()
+        assert st["misses"] == s_ref[-1][2] and st["evicted"] == s_ref[-1][10]
+        assert st["disk_reads"] == x_ref[-1][0] > 0 and st["disk_read_bytes"] == x_ref[-1][1]
+        assert st["disk_drops"] == x_ref[-1][3] and st["disk_discards"] == x_ref[-1][4]
+        assert st["disk_units"] == x_ref[-1][5]
+        run.ctx.check()
+        for L in range(m.layers):
+            for u in range(m.units):
+                run.ctx.check_unit(L, u)
+    finally:
+        run.close()
+
+
+def test_file_tier_predictions_read_files(small_model, orc, ref, monkeypatch):
+    """dg_disk_prefetch: predictions read file units too (on the prefetch stream, covered by the demand's wait)."""
+    monkeypatch.setenv("TSB_DG_DETERMINISTIC", "1")
+    m = small_model
+    ids = synth.zipf_trace(30, m.layers, m.units, 2, s=0.8, seed=23)
+    preds = synth.zipf_trace(30, m.layers, m.units, 2, s=0.8, seed=24)
+    run, res, disk = file_tier_run(m, pinned=2, S=2, n_pred=2, disk_prefetch=1)
+    try:
+        cfg = file_tier_cfg(run, m, res, disk, ids, 2, n_pred=2, disk_prefetch=1)
+        x_ref = np.zeros((ids.shape[0], 6), dtype=np.uint64)
+        t_ref, s_ref = oracle.ref_replay(cfg, ids, preds, xstats=x_ref)
+        want = expected_sums(m, orc)
+        for t in range(ids.shape[0]):
+            got = run.step(ids[t], preds[t])
+            keys = np.arange(m.layers)[:, None] * m.units + ids[t]
+            assert np.array_equal(got, want[keys]), "token %d read wrong bytes" % t
+            assert np.array_equal(run.ctx.table(run.keys), t_ref[t]), "slot table differs after token %d" % t
+        st = run.ctx.stats()
+        assert st["prefetched"] == s_ref[-1][5] > 0 and st["disk_reads"] == x_ref[-1][0]
+    finally:
+        run.close()
+
+
+def test_file_tier_reset_open_reads_files_back(small_model, orc, monkeypatch):
+    """ss_dg_reset_open with the file tier: units whose open home is their file give up their slot or block, units
+    that came from their file to an open slot or block are read back; the open placement and every byte return."""
+    monkeypatch.setenv("TSB_DG_DETERMINISTIC", "1")
+    m = small_model
+    run, _, _ = file_tier_run(m, R=2, pinned=3, S=2)
+    try:
+        open_table = run.ctx.table(run.keys).copy()
+        want = expected_sums(m, orc)
+        run_tokens(run, synth.zipf_trace(25, m.layers, m.units, 2, s=0.5, seed=29), want)
+        assert run.ctx.stats()["disk_reads"] > 0
+        assert not np.array_equal(run.ctx.table(run.keys), open_table)
+        run.ctx.reset_open()
+        assert np.array_equal(run.ctx.table(run.keys), open_table)
+        run.ctx.check()
+        for L in range(m.layers):
+            for u in range(m.units):
+                run.ctx.check_unit(L, u)
+        run_tokens(run, synth.zipf_trace(5, m.layers, m.units, 2, s=0.5, seed=30), want)
+    finally:
+        run.close()

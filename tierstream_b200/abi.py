@@ -114,7 +114,14 @@ _DG_STATS_U64_1 = ["tokens", "lookups", "misses", "covered", "fetched", "prefetc
                    "stalled", "free_slots", "blocks", "slots", "predicted", "predicted_true", "miss_layers",
                    "device_timeouts", "covered_waits", "wb_deferred", "wb_cancelled", "wb_forced",
                    "wb_boundary_flushed", "wb_issued_bytes", "wb_completed_bytes", "wb_cancelled_bytes",
-                   "wb_boundary_flushed_bytes", "wb_outstanding_bytes", "wb_forced_wait_ns"]
+                   "wb_boundary_flushed_bytes", "wb_outstanding_bytes", "wb_forced_wait_ns",
+                   "winpf_hints", "winpf_hint_rows", "prior_issued", "prior_used", "prior_late", "prior_reverted",
+                   "l1_candidates", "l1_issued", "l1_used", "l1_late", "l1_reverted", "l1_priced_out",
+                   "l1_skipped_ahead", "prior_budget_stops", "score_fallbacks", "scored_victims", "score_layers",
+                   "score_candidates", "score_saturated", "score_ns", "score_deferred", "score_last_ns",
+                   "disk_reads", "disk_read_bytes", "disk_read_ns", "disk_stage_waits", "disk_drops", "disk_discards",
+                   "inclusive_kept", "inclusive_drops", "disk_units", "backed_units", "disk_wait_ns",
+                   "disk_overlapped", "disk_max_in_flight", "disk_carried", "disk_carried_bytes"]
 
 
 class ss_dg_stats(C.Structure):

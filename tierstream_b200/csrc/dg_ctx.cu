@@ -20,6 +20,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <functional>
 #include <memory>
 #include <mutex>
 #include <thread>
@@ -101,6 +102,10 @@ struct Layout {
   uint32_t keys = 0, R = 0, D = 0, B = 0, P = 0, Q = 0, I = 0;
   uint32_t persistent_slots = 0, slots = 0, guard_slot = 0, blocks = 0;
   std::vector<uint32_t> residents;  // keys of tier R, key order
+  // file tier (dg_disk_tier): F units of tier DISK (flagged per key in `disk`), S staging buffers after the blocks
+  bool disk_tier = false, disk_prefetch = false;
+  uint32_t F = 0, S = 0;
+  std::vector<uint8_t> disk;
 };
 
 Layout make_layout(const Desc& d, const Plan& p, const ss_options& o, const PeerTier* peer) {
@@ -119,8 +124,17 @@ Layout make_layout(const Desc& d, const Plan& p, const ss_options& o, const Peer
   if (o.dg_wait_timeout_ms < 1) refuse(SS_E_INVALID, "dg_wait_timeout_ms must be >= 1");
   if (o.dg_wb_defer > 1) refuse(SS_E_INVALID, "dg_wb_defer must be 0 or 1");
   if (o.dg_wb_stream > 1) refuse(SS_E_INVALID, "dg_wb_stream must be 0 or 1");
-  if (o.dg_disk_tier || o.dg_disk_prefetch || o.dg_disk_staging || o.dg_disk_queue)
-    refuse(SS_E_UNSUPPORTED, "the three-tier placement (dg_disk_*) is not in this build");
+  // the file tier with synchronous reads (dg_disk_queue 0 or 1), as the reference checks its options
+  // (dg_layout.cpp:200-207); a read queue (> 1 or SS_DG_DISK_QUEUE_AUTO) is not in this build
+  constexpr uint32_t kQueueAuto = 0xFFFFFFFFu;
+  if (o.dg_disk_tier > 1 || o.dg_disk_prefetch > 1) refuse(SS_E_INVALID, "dg_disk_tier / dg_disk_prefetch must be 0 or 1");
+  if (!o.dg_disk_tier && (o.dg_disk_prefetch || o.dg_disk_staging || (o.dg_disk_queue && o.dg_disk_queue != kQueueAuto)))
+    refuse(SS_E_INVALID, "dg_disk_prefetch / dg_disk_staging / dg_disk_queue need dg_disk_tier = 1");
+  if (o.dg_disk_staging > 256) refuse(SS_E_INVALID, "dg_disk_staging must be 0..256");
+  if (o.dg_disk_tier && o.dg_disk_queue > 1)
+    refuse(SS_E_UNSUPPORTED, "dg_disk_queue above 1 (file reads in flight across calls) is not in this build: use 0 or 1 "
+                             "(one read at a time inside its fetch)");
+  if (o.dg_disk_tier && peer) refuse(SS_E_UNSUPPORTED, "the file tier with the peer tier is not in this build");
   if (o.dg_no_admit || o.dg_clean_evict || o.dg_pf_revert_unused || o.dg_pf_strict_admit || o.dg_landing_blocks ||
       o.dg_bank_keep || o.dg_disk_queue_adapt || o.dg_prior_len || o.dg_score_profile_len)
     refuse(SS_E_UNSUPPORTED, "an opt-in device-gated policy of the reference that is not in this build is set");
@@ -170,10 +184,13 @@ Layout make_layout(const Desc& d, const Plan& p, const ss_options& o, const Peer
         ++planned;
       } else if (t == SS_TIER_PINNED) {
         ++x.P;
+      } else if (t == SS_TIER_DISK && o.dg_disk_tier) {
+        ++x.F;
       } else {
         refuse(SS_E_CAPACITY, "unit (" + std::to_string(l.index) + ", " + std::to_string(u) +
                                   ") is not resident or pinned (no gated unit is read from its file)");
       }
+      if (o.dg_disk_tier) x.disk.push_back(t == SS_TIER_DISK ? 1 : 0);
     }
     x.D += std::min<uint32_t>(b.dynamic_slots_per_layer, uint32_t(l.n_units) - planned);
     keys += uint64_t(l.n_units);
@@ -182,10 +199,13 @@ Layout make_layout(const Desc& d, const Plan& p, const ss_options& o, const Peer
   }
   x.keys = uint32_t(keys);
   x.R = uint32_t(x.residents.size());
+  x.disk_tier = o.dg_disk_tier != 0;
+  x.disk_prefetch = o.dg_disk_prefetch != 0;
+  x.S = x.disk_tier ? (o.dg_disk_staging ? o.dg_disk_staging : 8u) : 0u;
   if (o.dg_spare_slots) {
-    if (o.dg_spare_slots > x.P)
+    if (o.dg_spare_slots > x.P + x.F)
       refuse(SS_E_INVALID, "dg_spare_slots " + std::to_string(o.dg_spare_slots) + " above the non-resident units (" +
-                               std::to_string(x.P) + ")");
+                               std::to_string(x.P + x.F) + ")");
     x.D = o.dg_spare_slots;
   }
   if (x.D < 1)
@@ -224,8 +244,8 @@ Layout make_layout(const Desc& d, const Plan& p, const ss_options& o, const Peer
     refuse(SS_E_CAPACITY, "the arena needs " + std::to_string(need) + " bytes where the plan billed " +
                               std::to_string(billed) + "; with the rest of the plan that is above the cap - margin");
   const bool no_blocks = peer && peer->all_owned;  // every unit in a store: no pinned block is allocated
-  if (!no_blocks && p.pinned + x.host_stride + (uint64_t(1) << 20) > b.host_pinned_bytes)
-    refuse(SS_E_CAPACITY, "the plan's pinned bytes plus the staging unit and the mapped control area exceed the host "
+  if (!no_blocks && p.pinned + (1ull + x.S) * x.host_stride + (uint64_t(1) << 20) > b.host_pinned_bytes)
+    refuse(SS_E_CAPACITY, "the plan's pinned bytes plus the staging units and the mapped control area exceed the host "
                           "budget (" + std::to_string(b.host_pinned_bytes) + ")");
   return x;
 }
@@ -354,6 +374,12 @@ class CudaMover final : public Mover {
     ck_launch(dev::move_take_timeouts(&timeouts), "move kernel timeout word");
     require(!timeouts, SS_E_BACKEND, "device-gated: a staging copy of the move kernel did not complete");
   }
+  // File tier: the unit from its file into a block or staging buffer (the context's checked read), synchronously.
+  void read_unit(uint32_t key, int32_t block) override {
+    require(reader_ != nullptr, SS_E_BACKEND, "device-gated: no file reader");
+    reader_(key, block_host(block));
+  }
+  void set_reader(std::function<void(uint32_t, char*)> f) { reader_ = std::move(f); }
   void h2h(int32_t src, int32_t dst, uint32_t key) override {
     if (peer_ && peer_->owned(key)) return;
     std::memcpy(block_host(dst), block_host(src), size_t(x_.unit_bytes));
@@ -498,6 +524,7 @@ class CudaMover final : public Mover {
   const Layout& x_;
   Buffers b_;
   const PeerTier* peer_ = nullptr;
+  std::function<void(uint32_t, char*)> reader_;
   uint64_t peer_units_ = 0, self_units_ = 0;
   cudaStream_t s_[3] = {nullptr, nullptr, nullptr};
   int32_t* table_pin_ = nullptr;
@@ -862,6 +889,10 @@ class CudaDgContext final : public DgContext {
     require(unit >= 0 && uint32_t(unit) < core_->units(uint32_t(g)), SS_E_INVALID, "ss_check_unit: unit out of range");
     core_->drain();
     const uint32_t k = core_->key(uint32_t(g), uint32_t(unit));
+    if (core_->home(k) == SlotCache::Home::File) {  // its only copy is its file
+      core_->check();
+      return;
+    }
     std::vector<char> got(size_t(x_.unit_bytes)), want(size_t(x_.unit_bytes));
     if (core_->slot_of(k) >= 0 &&
         (core_->home(k) == SlotCache::Home::Device || core_->home(k) == SlotCache::Home::Evicting)) {
@@ -1052,6 +1083,16 @@ class CudaDgContext final : public DgContext {
     s.inclusive_kept = d(c.inclusive_kept, base_.inclusive_kept);
     s.inclusive_drops = d(c.inclusive_drops, base_.inclusive_drops);
     s.backed_units = core_->backed_units();
+    s.disk_reads = d(c.disk_reads, base_.disk_reads);
+    s.disk_read_bytes = d(c.disk_read_bytes, base_.disk_read_bytes);
+    s.disk_read_ns = d(c.disk_read_ns, base_.disk_read_ns);
+    s.disk_wait_ns = s.disk_read_ns;  // synchronous reads: the service waits for each one whole
+    s.disk_stage_waits = d(c.disk_stage_waits, base_.disk_stage_waits);
+    s.disk_drops = d(c.disk_drops, base_.disk_drops);
+    s.disk_discards = d(c.disk_discards, base_.disk_discards);
+    s.disk_units = core_->file_units();
+    s.disk_max_in_flight = c.disk_reads ? 1 : 0;  // (a gauge since open: one read at a time)
+    s.disk_queue_resolved = x_.disk_tier ? 1u : 0u;
     std::memcpy(out, &s, sizeof s);
   }
   void layer_stats(int layer, ss_layer_stats* out) const override {
@@ -1095,7 +1136,7 @@ class CudaDgContext final : public DgContext {
     ss_exclusive_stats s{};
     s.struct_size = uint32_t(sizeof s);
     const CacheStats& c = core_->stats();
-    s.writebacks = c.evicted - c.wb_cancelled - c.inclusive_drops;
+    s.writebacks = c.evicted - c.wb_cancelled - c.inclusive_drops - c.disk_discards;
     s.writeback_bytes = c.wb_issued_bytes;
     s.free_blocks = core_->free_blocks();
     s.min_free_blocks = core_->free_blocks();
@@ -1110,7 +1151,9 @@ class CudaDgContext final : public DgContext {
                   "\"dg\":{\"tokens\":%llu,\"lookups\":%llu,\"misses\":%llu,\"covered\":%llu,\"fetched\":%llu,"
                   "\"prefetched\":%llu,\"bank_serves\":%llu,\"evicted\":%llu,\"resurrected\":%llu,"
                   "\"writebacks_done\":%llu,\"wb_issued_bytes\":%llu,\"free_slots\":%llu,\"land_launches\":%llu,"
-                  "\"dma_ms_total\":%.6f,\"open_seconds\":%.3f},\"peer\":{\"world\":%u,\"rank\":%d,"
+                  "\"dma_ms_total\":%.6f,\"open_seconds\":%.3f,\"disk_reads\":%llu,\"disk_read_bytes\":%llu,"
+                  "\"disk_read_ns\":%llu,\"disk_drops\":%llu,\"disk_discards\":%llu,\"disk_units\":%llu},"
+                  "\"peer\":{\"world\":%u,\"rank\":%d,"
                   "\"all_owned\":%d,\"copy\":\"%s\",\"peer_units\":%llu,\"self_units\":%llu},"
                   "\"open\":{\"alloc_s\":%.3f,\"fill_pinned_s\":%.3f,\"fill_residents_s\":%.3f,\"verify_s\":%.3f}}",
                   mover_->kernel_copies() ? "land-kernel" : "copy-engine", (unsigned long long)s.tokens,
@@ -1119,7 +1162,10 @@ class CudaDgContext final : public DgContext {
                   (unsigned long long)s.evicted, (unsigned long long)s.resurrected,
                   (unsigned long long)s.writebacks_done, (unsigned long long)s.wb_issued_bytes,
                   (unsigned long long)s.free_slots, (unsigned long long)mover_->kernel_launches(),
-                  mover_->dma_total_ms(), open_seconds_, peer_ ? peer_->world : 0u, peer_ ? peer_->rank : -1,
+                  mover_->dma_total_ms(), open_seconds_, (unsigned long long)s.disk_reads,
+                  (unsigned long long)s.disk_read_bytes, (unsigned long long)s.disk_read_ns,
+                  (unsigned long long)s.disk_drops, (unsigned long long)s.disk_discards,
+                  (unsigned long long)s.disk_units, peer_ ? peer_->world : 0u, peer_ ? peer_->rank : -1,
                   peer_ && peer_->all_owned ? 1 : 0, peer_ && peer_->copy == 1 ? "copy-engine" : "land-kernel",
                   (unsigned long long)mover_->peer_units(), (unsigned long long)mover_->self_units(), open_alloc_s_,
                   open_fill_pinned_s_, open_fill_res_s_, open_verify_s_);
@@ -1224,6 +1270,16 @@ class CudaDgContext final : public DgContext {
       off += p.bytes;
     }
   }
+  // A file-tier read: with verify_hash and descriptor hashes, the bytes are checked on the host before any copy reads
+  // them (the reference's read_checked, dg_ctx.cpp:1625-1633).
+  void read_checked(int layer, int unit, char* dst) const {
+    read_unit(layer, unit, dst);
+    const Layer& l = d_.layers[size_t(layer)];
+    if (o_.verify_hash && !l.hash.empty())
+      require(xxh64(dst, size_t(x_.unit_bytes)) == l.hash[size_t(unit)], SS_E_HASH,
+              "device-gated: unit (" + std::to_string(layer) + ", " + std::to_string(unit) +
+                  ") bytes differ from the descriptor hash");
+  }
 
   void init() {
     auto t_start = Clock::now();
@@ -1309,12 +1365,13 @@ class CudaDgContext final : public DgContext {
     gpu_wait_us_.assign(G, -1);
     gpu_ready_us_.assign(G, -1);
     // pinned blocks (mapped: the land kernel reads them) in <= 1 GiB chunks (pinned.cu: mapped, populated by a pool of
-    // threads with huge pages, registered); the reset staging unit
+    // threads with huge pages, registered), the file tier's staging buffers after them (block indices blocks ..);
+    // the reset staging unit
     const uint64_t hs = x_.host_stride;
     const uint64_t per_chunk = std::max<uint64_t>(1, (uint64_t(1) << 30) / hs);
     std::vector<uint64_t> chunk_units;
     std::vector<size_t> chunk_bytes;
-    for (uint64_t left = peer_ && peer_->all_owned ? 0 : x_.blocks; left > 0;) {
+    for (uint64_t left = peer_ && peer_->all_owned ? 0 : uint64_t(x_.blocks) + x_.S; left > 0;) {
       chunk_units.push_back(std::min(per_chunk, left));
       chunk_bytes.push_back(size_t(chunk_units.back() * hs));
       left -= chunk_units.back();
@@ -1355,6 +1412,16 @@ class CudaDgContext final : public DgContext {
     c.wb_layer_bytes = o_.dg_wb_layer_bytes;
     c.wb_max_outstanding = o_.dg_wb_max_outstanding;
     c.inclusive = x_.I;
+    c.disk_tier = x_.disk_tier;
+    c.disk_prefetch = x_.disk_prefetch;
+    c.home_blocks = x_.disk_tier ? x_.P : 0;  // the plan's pinned units get the blocks; the rest are spares
+    c.disk_staging = x_.S;
+    if (x_.disk_tier)  // a file miss: the unit's parts from their files, checked against the descriptor's hash
+      mover_->set_reader([this](uint32_t key, char* dst) {
+        const uint32_t g = uint32_t(std::upper_bound(x_.unit_base.begin(), x_.unit_base.end(), key) -
+                                    x_.unit_base.begin()) - 1;
+        read_checked(x_.gated[g], int(key - x_.unit_base[g]), dst);
+      });
     core_ = std::make_unique<SlotCache>(c, mover_.get());
     std::vector<uint32_t> order;
     if (o_.dg_seed_n) {
@@ -1370,7 +1437,7 @@ class CudaDgContext final : public DgContext {
     o_.dg_seed_n = 0;
     order.insert(order.end(), x_.residents.begin(), x_.residents.end());
     for (uint32_t k = 0; k < x_.keys; ++k) order.push_back(k);
-    core_->place(order);
+    core_->place(order, x_.disk_tier ? &x_.disk : nullptr);
     open_alloc_s_ = std::chrono::duration<double>(Clock::now() - t_start).count();
     fill();
     mover_->upload_table(core_->table().data(), x_.keys);
@@ -1396,7 +1463,7 @@ class CudaDgContext final : public DgContext {
         const uint32_t k = core_->key(g, u);
         const bool owned = peer_ && peer_->owned(k);  // an owned unit's block is never read: not filled
         if (core_->slot_of(k) >= 0) (owned ? from_store : res).push_back({g, u});
-        else if (!owned) pin.push_back({g, u});
+        else if (!owned && core_->block_of(k) >= 0) pin.push_back({g, u});  // (a file home stays in its file)
       }
     const bool verify = o_.verify_hash != 0;
     unsigned nthreads = std::max(1u, std::min(16u, std::thread::hardware_concurrency()));

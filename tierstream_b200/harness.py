@@ -16,7 +16,7 @@ class DgRun:
     def __init__(self, model, residents_per_layer=None, resident_keys=None, spare_per_layer=1, max_ids=2,
                  host_spare_units=None, diag=False, test_hooks=True, wb_defer=1, wb_stream=1, verify=False,
                  n_pred=0, slices=64, mode=0, timeout_ms=10000, device_bytes=None, with_reader=True,
-                 resident_order=None, inclusive=0, peer=None):
+                 resident_order=None, inclusive=0, peer=None, disk_keys=(), disk_staging=0, disk_prefetch=0):
         self.model = model
         G, U = model.layers, model.units
         self.G, self.U, self.n_ids, self.n_pred = G, U, max_ids, n_pred
@@ -28,7 +28,10 @@ class DgRun:
                 resident_keys += [g * U + e for e in order[:residents_per_layer]]
         for k in resident_keys:
             tiers[k] = abi.SS_TIER_RESIDENT
+        for k in disk_keys:  # the file tier: these units live in their files only
+            tiers[k] = abi.SS_TIER_DISK
         self.resident_keys = list(resident_keys)
+        self.disk_keys = list(disk_keys)
         b = abi.budget_defaults()
         unit = model.unit_bytes
         slots = len(resident_keys) + spare_per_layer * G + 2 * max_ids + 1
@@ -40,7 +43,8 @@ class DgRun:
         b.ring_slots = 2 * max_ids + 1
         b.host_spare_units = host_spare_units if host_spare_units is not None else spare_per_layer * G + inclusive
         hs = (unit + 4095) // 4096 * 4096
-        b.host_pinned_bytes = (G * U - len(resident_keys) + b.host_spare_units + 2) * hs + (64 << 20)
+        b.host_pinned_bytes = (G * U - len(resident_keys) - len(self.disk_keys) + b.host_spare_units + 2 +
+                               ((disk_staging or 8) if self.disk_keys else 0)) * hs + (64 << 20)
         self.desc = runtime.Desc(model.desc())
         self.plan = runtime.Plan(self.desc, b, tiers=tiers)
         o = abi.options_defaults()
@@ -54,6 +58,10 @@ class DgRun:
         o.verify_hash = 1 if verify else 0
         o.dg_wait_timeout_ms = timeout_ms
         o.dg_inclusive_blocks = inclusive
+        if self.disk_keys:
+            o.dg_disk_tier = 1
+            o.dg_disk_staging = disk_staging
+            o.dg_disk_prefetch = disk_prefetch
         o.device = torch.cuda.current_device()  # the context lives on the engine's device
         self.ctx = runtime.DgContext(self.desc, self.plan, o, peer=peer)
         self.stream = torch.cuda.Stream()
