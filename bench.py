@@ -10,7 +10,9 @@ Printed metric: expert-miss stream GB/s = bytes landed by the miss service (dema
 decode, aggregated over ranks. N > 1 (one process per GPU) runs the peer tier by default ("mixtral-8x7b-dg-peer"):
 each rank decodes its own trace, every expert is owned by one rank's HBM store (owners planned from the ranks' summed
 routing counts, one NCCL all-reduce), and a miss is copied from its owner's store over NVLink (or from the rank's own
-store) instead of pinned RAM; `--tier pinned` runs N independent pinned-RAM replicas instead.
+store) instead of pinned RAM; `--tier pinned` runs N independent pinned-RAM replicas instead. `--tier file` (one GPU)
+runs the file tier ("mixtral-8x7b-dg-file"): every non-resident expert lives in the model file only and a miss reads
+it (O_DIRECT) into a pinned staging buffer, then copies it to HBM.
 `value` is device time (CUDA events on the engine stream) with the routed ids already in HBM; `e2e` is the same steps
 through the public ABI with the ids copied from pinned host memory and the readers' results copied back each step,
 timed by the host clock. `--impl reference` times the reference's own DgCore (compiled from its sources) with a host
@@ -62,11 +64,15 @@ def args_():
                    help="spare slots per layer (dynamic_slots_per_layer); 0 = the workload's (1 Mixtral, 4 Qwen3)")
     p.add_argument("--cpu-sample-tokens", type=int, default=6)
     p.add_argument("--no-cpu-baseline", action="store_true")
-    p.add_argument("--tier", default="auto", choices=["auto", "pinned", "peer"],
+    p.add_argument("--tier", default="auto", choices=["auto", "pinned", "peer", "file"],
                    help="where non-resident experts live: pinned RAM, or the peer tier (every expert owned by one "
                         "rank's HBM store, owners planned from the ranks' summed routing counts by one all-reduce; a "
-                        "miss is copied from its owner's store, NVLink for a peer, HBM for the rank's own); auto = "
-                        "pinned at one GPU, peer at several")
+                        "miss is copied from its owner's store, NVLink for a peer, HBM for the rank's own), or the "
+                        "file tier (one GPU: in the model file only, read on a miss through a pinned staging buffer); "
+                        "auto = pinned at one GPU, peer at several")
+    p.add_argument("--pinned-per-layer", type=int, default=0,
+                   help="file tier: non-resident experts per layer that keep a pinned block (the rest in the file)")
+    p.add_argument("--staging", type=int, default=4, help="file tier: staging buffers (ss_options.dg_disk_staging)")
     p.add_argument("--workload", default="mixtral-8x7b-dg", choices=["mixtral-8x7b-dg", "qwen3-235b-a22b-peer"],
                    help="mixtral-8x7b-dg: BASELINE configs[1] (default); qwen3-235b-a22b-peer: configs[4], the peer "
                         "tier on 4 or more GPUs")
@@ -194,7 +200,47 @@ def hbm_copy_peak():
 
 
 def inclusive_of(a):
+    if a.tier == "file":
+        return 0 if a.inclusive < 0 else a.inclusive
     return LAYERS * UNITS - RESIDENTS if a.inclusive < 0 else a.inclusive
+
+
+def disk_keys(a, residents):
+    """File tier: per layer every non-resident expert except the first --pinned-per-layer by popularity."""
+    from tierstream_b200 import synth
+    pop = synth.popularity_order(LAYERS, UNITS, s=ZIPF, seed=1)
+    res = set(residents)
+    out = []
+    for g in range(LAYERS):
+        rest = [g * UNITS + e for e in pop[g] if g * UNITS + e not in res]
+        out += rest[a.pinned_per_layer:]
+    return out
+
+
+def file_read_peak(path, nbytes=2 << 30, piece=33030144):
+    """One thread's sequential O_DIRECT read rate of the model file (GB/s), in unit parts as the file tier reads them
+    (the file tier's synchronous reads run one at a time); None when O_DIRECT is refused here."""
+    import mmap
+    try:
+        fd = os.open(path, os.O_RDONLY | os.O_DIRECT)
+    except OSError:
+        return None
+    try:
+        buf = mmap.mmap(-1, piece)
+        size = os.fstat(fd).st_size
+        off, got, t0 = 0, 0, time.perf_counter()
+        while got < nbytes and off + piece <= size:
+            n = os.preadv(fd, [buf], off)
+            if n <= 0:
+                break
+            got += n
+            off += piece
+        dt = time.perf_counter() - t0
+        return got / dt / 1e9 if got and dt > 0 else None
+    except OSError:
+        return None
+    finally:
+        os.close(fd)
 
 
 def reference_sample(ids, tokens, a):
@@ -260,6 +306,9 @@ def main():
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     a.peer = a.tier == "peer" or (a.tier == "auto" and world > 1)
+    a.file = a.tier == "file"
+    if a.file and (world > 1 or a.workload != "mixtral-8x7b-dg"):
+        raise SystemExit("--tier file runs the Mixtral-shaped workload on one GPU")
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
@@ -284,6 +333,7 @@ def main():
             model.write()
     barrier()
     peak = h2d_peak(torch) if rank == 0 and not a.peer else None
+    read_peak = file_read_peak(model_path()) if a.file else None
     ids = synth.zipf_trace(a.warmup + a.steps, LAYERS, UNITS, TOP_K, s=ZIPF, seed=1 + rank)
     inclusive = 0 if a.peer else inclusive_of(a)
     t_open = time.perf_counter()
@@ -316,7 +366,8 @@ def main():
                                    collective_device=torch.device("cuda", local) if dist else None, filler=filler)
     run = harness.DgRun(model, resident_keys=resident_keys(1 + rank), spare_per_layer=a.spare, max_ids=TOP_K,
                         diag=True, test_hooks=False, mode=1, slices=128, wb_defer=a.wb_defer, wb_stream=a.wb_stream,
-                        inclusive=inclusive, peer=setup.tier if setup else None)
+                        inclusive=inclusive, peer=setup.tier if setup else None,
+                        disk_keys=disk_keys(a, resident_keys(1)) if a.file else (), disk_staging=a.staging)
     t_open = time.perf_counter() - t_open
     unit = model.unit_bytes
     try:
@@ -371,7 +422,8 @@ def main():
         dg = {k: s1[k] - s0[k] for k in ("fetched", "prefetched", "bank_serves", "evicted", "evict_short",
                                          "writebacks_done", "collected_mid", "wb_forced", "wb_forced_wait_ns",
                                          "wb_boundary_flushed", "wb_deferred", "wb_cancelled", "resurrected",
-                                         "wb_issued_bytes", "covered")}
+                                         "wb_issued_bytes", "covered", "disk_reads", "disk_read_bytes",
+                                         "disk_read_ns", "disk_drops", "disk_discards")}
         full = json.loads(run.ctx.stats_json())
         peer_stats, open_stats = full["peer"], full["open"]
     finally:
@@ -445,6 +497,25 @@ def main():
                            "has no NVLink figure) for the %d units pulled from peers and the measured HBM copy rate "
                            "(MEASURED_PEAKS.json hbm_gbs / 2 = %.1f GB/s) for the %d units copied from the rank's own "
                            "store, rank 0's timed tokens" % (peer_units, hbm_copy, self_units)})
+    if a.file:
+        # a file miss is a synchronous O_DIRECT read into a staging buffer, then its copy to HBM: the ideal mover does
+        # the two back to back, each at its measured rate
+        rd = dg["disk_read_bytes"] / (dg["disk_read_ns"] / 1e9) / 1e9 if dg["disk_read_ns"] else None
+        peak_file = 1.0 / (1.0 / read_peak + 1.0 / peak) if read_peak and peak else None
+        line["config"].update({"workload": "mixtral-8x7b-dg-file", "pinned_per_layer": a.pinned_per_layer,
+                               "staging": a.staging, "file_units": LAYERS * UNITS - RESIDENTS -
+                               a.pinned_per_layer * LAYERS})
+        line["file_tier"] = {"disk_read_gbs": round(rd, 3) if rd else None,
+                             "file_read_peak_gbs": round(read_peak, 3) if read_peak else None,
+                             "reads_per_token": round(dg["disk_reads"] / a.steps, 3)}
+        line["roofline"].update({
+            "bound": "file+link", "kernel": "miss service (file read into staging, then the copy, entries and ready)",
+            "peak": round(peak_file, 3) if peak_file else None,
+            "frac": round(achieved / peak_file, 4) if achieved and peak_file else None,
+            "peak_source": "one read then one copy per miss at the rates measured in this run: sequential O_DIRECT "
+                           "reads of the model file in 33 MB parts on one thread, and the copy-engine pinned->HBM "
+                           "rate"})
+        a.no_cpu_baseline = True  # the reference arm's sample is the pinned-RAM configuration
     if not a.no_cpu_baseline and world == 1:
         smp = a.cpu_sample_tokens
         mv, dt = reference_sample(synth.zipf_trace(smp, LAYERS, UNITS, TOP_K, s=ZIPF, seed=1), smp, a)
