@@ -95,6 +95,12 @@ SS_API ss_status tsb_test_dg_table(ss_ctx* c, int32_t* out, uint32_t cap);
  * (-1 for no entry). n must be the layer's units. */
 SS_API ss_status tsb_test_host_locs(ss_ctx* c, int layer, int32_t* out, int n);
 
+/* Test hook: [offset, offset + bytes) of the file at `path` into dst in pieces of `piece` bytes read by a pool of
+ * `threads` reader threads (the file tier's reads), unbuffered (O_DIRECT, straight into dst when aligned) when direct
+ * is set and the file system allows it. */
+SS_API ss_status tsb_test_file_read(const char* path, uint64_t offset, uint64_t bytes, void* dst, uint64_t piece,
+                                    uint32_t threads, int direct);
+
 /* ---- Host xxh64 (this library's, the one the open's fill checks pinned units with; seed 0 in the descriptor) ---- */
 SS_API uint64_t tsb_xxh64(const void* data, size_t len, uint64_t seed);
 

@@ -216,6 +216,7 @@ _PROTOS = {
     "tsb_land": (C.c_int, [P(vp), P(vp), P(u64), u32, vp, P(u32), P(i32), u32, vp, u32, vp, u32, vp]),
     "tsb_move": (C.c_int, [P(vp), P(vp), P(u64), u32, vp, P(u32), P(i32), u32, vp, u32, vp, u32, vp]),
     "tsb_move_timeouts": (C.c_int, []),
+    "tsb_test_file_read": (C.c_int, [C.c_char_p, u64, u64, vp, u64, u32, C.c_int]),
     "tsb_xxh64_units": (C.c_int, [P(vp), P(u64), P(u32), u32, vp, vp, vp, vp, vp]),
     "tsb_xxh64_units_static": (C.c_int, [P(vp), P(u64), P(u32), u32, vp, vp, vp, vp]),
     "tsb_peer_plan": (C.c_int, [P(u64), u32, u32, P(u64), P(C.c_int32)]),

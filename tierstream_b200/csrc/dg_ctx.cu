@@ -1270,11 +1270,25 @@ class CudaDgContext final : public DgContext {
       off += p.bytes;
     }
   }
-  // A file-tier read: with verify_hash and descriptor hashes, the bytes are checked on the host before any copy reads
-  // them (the reference's read_checked, dg_ctx.cpp:1625-1633).
+  // A file-tier read: the unit's parts in pieces of at most 8 MiB, read by the reader pool at once (the reference
+  // reads a unit in one pass on one reader); with verify_hash and descriptor hashes, the bytes are checked on the host
+  // before any copy reads them (the reference's read_checked, dg_ctx.cpp:1625-1633).
   void read_checked(int layer, int unit, char* dst) const {
-    read_unit(layer, unit, dst);
     const Layer& l = d_.layers[size_t(layer)];
+    struct Piece {
+      const SourceFile* f;
+      uint64_t off, bytes;
+      char* dst;
+    };
+    std::vector<Piece> pieces;
+    uint64_t at = 0;
+    for (const Part& p : l.parts) {
+      const uint64_t base = p.offset + uint64_t(unit) * p.stride;
+      for (uint64_t o = 0; o < p.bytes; o += kReadPiece)
+        pieces.push_back({files_[size_t(p.source)].get(), base + o, std::min(kReadPiece, p.bytes - o), dst + at + o});
+      at += p.bytes;
+    }
+    readers_->run(pieces.size(), [&](size_t i) { pieces[i].f->read(pieces[i].dst, pieces[i].off, pieces[i].bytes); });
     if (o_.verify_hash && !l.hash.empty())
       require(xxh64(dst, size_t(x_.unit_bytes)) == l.hash[size_t(unit)], SS_E_HASH,
               "device-gated: unit (" + std::to_string(layer) + ", " + std::to_string(unit) +
@@ -1416,12 +1430,16 @@ class CudaDgContext final : public DgContext {
     c.disk_prefetch = x_.disk_prefetch;
     c.home_blocks = x_.disk_tier ? x_.P : 0;  // the plan's pinned units get the blocks; the rest are spares
     c.disk_staging = x_.S;
-    if (x_.disk_tier)  // a file miss: the unit's parts from their files, checked against the descriptor's hash
+    if (x_.disk_tier) {  // a file miss: the unit's parts from their files, checked against the descriptor's hash
+      unsigned n = 8;
+      if (const char* e = std::getenv("TSB_FILE_READERS")) n = unsigned(std::max(1L, std::min(64L, std::atol(e))));
+      readers_ = std::make_unique<ReadPool>(n);
       mover_->set_reader([this](uint32_t key, char* dst) {
         const uint32_t g = uint32_t(std::upper_bound(x_.unit_base.begin(), x_.unit_base.end(), key) -
                                     x_.unit_base.begin()) - 1;
         read_checked(x_.gated[g], int(key - x_.unit_base[g]), dst);
       });
+    }
     core_ = std::make_unique<SlotCache>(c, mover_.get());
     std::vector<uint32_t> order;
     if (o_.dg_seed_n) {
@@ -1602,6 +1620,7 @@ class CudaDgContext final : public DgContext {
     svc_.reset();
     core_.reset();
     mover_.reset();
+    readers_.reset();
     for (char* a : bufs_.arena) cudaFree(a);
     if (bufs_.slot_of) cudaFree(bufs_.slot_of);
     if (ctl_) cudaFree(ctl_);
@@ -1618,6 +1637,8 @@ class CudaDgContext final : public DgContext {
   Layout x_;
   int device_ = 0;
   std::vector<std::unique_ptr<SourceFile>> files_;
+  static constexpr uint64_t kReadPiece = uint64_t(8) << 20;  // file tier: the reader pool's piece
+  std::unique_ptr<ReadPool> readers_;                        // file tier: the reads of one miss at once
   CudaMover::Buffers bufs_;
   uint32_t* ctl_ = nullptr;
   void* mapped_h_ = nullptr;

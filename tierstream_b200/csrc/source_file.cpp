@@ -4,6 +4,7 @@
 #include <sys/stat.h>
 #include <unistd.h>
 
+#include <algorithm>
 #include <cerrno>
 #include <cstdlib>
 #include <cstring>
@@ -52,8 +53,29 @@ void SourceFile::read(void* dst, uint64_t offset, uint64_t bytes) const {
     pread_all(fd_buffered_, static_cast<char*>(dst), offset, bytes, path_);
     return;
   }
-  // unbuffered: aligned covering reads through a bounce buffer (at most 8 MiB per read)
   const uint64_t a = align_ < 4096 ? 4096 : align_;
+  if (((reinterpret_cast<uintptr_t>(dst) | offset | bytes) & (a - 1)) == 0) {  // aligned: straight into dst
+    char* out = static_cast<char*>(dst);
+    uint64_t pos = offset, left = bytes;
+    while (left) {
+      const ssize_t r = ::pread(fd_, out, size_t(left), off_t(pos));
+      if (r < 0 && errno == EINTR) continue;
+      if (r < 0 && errno == EINVAL) {  // refused after all: buffered for the rest
+        pread_all(fd_buffered_, out, pos, left, path_);
+        return;
+      }
+      require(r > 0, SS_E_IO, "short read of " + path_ + " at offset " + std::to_string(pos));
+      out += r;
+      pos += uint64_t(r);
+      left -= uint64_t(r);
+      if (uint64_t(r) % a != 0 && left) {  // a short unaligned piece: the rest buffered
+        pread_all(fd_buffered_, out, pos, left, path_);
+        return;
+      }
+    }
+    return;
+  }
+  // unbuffered: aligned covering reads through a bounce buffer (at most 8 MiB per read)
   const uint64_t piece = uint64_t(8) << 20;
   void* raw = nullptr;
   require(::posix_memalign(&raw, size_t(a), size_t(piece + 2 * a)) == 0, SS_E_NOMEM, "bounce buffer");
@@ -83,6 +105,69 @@ void SourceFile::read(void* dst, uint64_t offset, uint64_t bytes) const {
     pos += want;
     left -= want;
   }
+}
+
+ReadPool::ReadPool(unsigned threads) {
+  for (unsigned i = 1; i < std::max(1u, threads); ++i) th_.emplace_back([this] { loop(); });
+}
+
+ReadPool::~ReadPool() {
+  {
+    std::lock_guard<std::mutex> lk(mu_);
+    stop_ = true;
+  }
+  start_cv_.notify_all();
+  for (std::thread& t : th_) t.join();
+}
+
+void ReadPool::work() {
+  for (;;) {
+    const size_t i = next_.fetch_add(1);
+    if (i >= n_) return;
+    try {
+      (*fn_)(i);
+    } catch (...) {
+      std::lock_guard<std::mutex> lk(mu_);
+      if (!err_) err_ = std::current_exception();
+    }
+  }
+}
+
+void ReadPool::loop() {
+  uint64_t seen = 0;
+  for (;;) {
+    {
+      std::unique_lock<std::mutex> lk(mu_);
+      start_cv_.wait(lk, [&] { return stop_ || gen_ != seen; });
+      if (stop_) return;
+      seen = gen_;
+    }
+    work();
+    std::lock_guard<std::mutex> lk(mu_);
+    if (--busy_ == 0) done_cv_.notify_all();
+  }
+}
+
+void ReadPool::run(size_t n, const std::function<void(size_t)>& fn) {
+  {
+    std::lock_guard<std::mutex> lk(mu_);
+    fn_ = &fn;
+    n_ = n;
+    next_ = 0;
+    err_ = nullptr;
+    busy_ = th_.size();
+    ++gen_;
+  }
+  start_cv_.notify_all();
+  work();
+  std::exception_ptr err;
+  {
+    std::unique_lock<std::mutex> lk(mu_);
+    done_cv_.wait(lk, [&] { return busy_ == 0; });
+    err = err_;
+    fn_ = nullptr;
+  }
+  if (err) std::rethrow_exception(err);
 }
 
 }  // namespace tsb

@@ -1,11 +1,45 @@
 // A descriptor source file opened for reading: unbuffered (O_DIRECT) when asked and allowed, else buffered. Reads of
-// any offset and size; unbuffered reads go through an aligned bounce buffer of the file's alignment.
+// any offset and size; an unbuffered read lands directly in the destination when its address, offset and size are
+// aligned, else goes through an aligned bounce buffer of the file's alignment.
 #pragma once
 
+#include <atomic>
+#include <condition_variable>
 #include <cstdint>
+#include <exception>
+#include <functional>
+#include <mutex>
 #include <string>
+#include <thread>
+#include <vector>
 
 namespace tsb {
+
+// A fixed set of reader threads serving one job at a time: run(n, fn) calls fn(i) for every i in [0, n) on the
+// threads and the caller, returns once all calls finished and rethrows the first failure. One caller at a time.
+class ReadPool {
+ public:
+  explicit ReadPool(unsigned threads);
+  ~ReadPool();
+  ReadPool(const ReadPool&) = delete;
+  ReadPool& operator=(const ReadPool&) = delete;
+  void run(size_t n, const std::function<void(size_t)>& fn);
+  unsigned threads() const { return unsigned(th_.size()) + 1; }
+
+ private:
+  void loop();
+  void work();
+  std::mutex mu_;
+  std::condition_variable start_cv_, done_cv_;
+  std::vector<std::thread> th_;
+  const std::function<void(size_t)>* fn_ = nullptr;
+  size_t n_ = 0;
+  std::atomic<size_t> next_{0};
+  size_t busy_ = 0;
+  uint64_t gen_ = 0;
+  bool stop_ = false;
+  std::exception_ptr err_;
+};
 
 class SourceFile {
  public:

@@ -9,6 +9,7 @@
 #include "dg_core.hpp"
 #include "errors.hpp"
 #include "kernels.hpp"
+#include "source_file.hpp"
 #include "tierstream/tsb.h"
 #include "xxh64.hpp"
 
@@ -136,6 +137,21 @@ ss_status tsb_xxh64_units(const void* const* spans, const uint64_t* span_bytes, 
 ss_status tsb_test_dg_replay(const tsb_dg_replay_config* cfg, const int32_t* ids, const int32_t* preds,
                              int32_t* tables, uint64_t* stats, const uint8_t* src_units, uint64_t* read_sum) {
   return run([&] { tsb::dg_replay(cfg, ids, preds, tables, stats, src_units, read_sum); });
+}
+
+ss_status tsb_test_file_read(const char* path, uint64_t offset, uint64_t bytes, void* dst, uint64_t piece,
+                             uint32_t threads, int direct) {
+  return run([&] {
+    tsb::require(path && (dst || !bytes) && piece >= 1 && threads >= 1 && threads <= 64, SS_E_INVALID,
+                 "tsb_test_file_read: bad argument");
+    tsb::SourceFile f(path, 4096, direct != 0);
+    tsb::ReadPool pool(threads);
+    const uint64_t n = (bytes + piece - 1) / piece;
+    pool.run(size_t(n), [&](size_t i) {
+      const uint64_t o = uint64_t(i) * piece;
+      f.read(static_cast<char*>(dst) + o, offset + o, std::min(piece, bytes - o));
+    });
+  });
 }
 
 uint64_t tsb_xxh64(const void* data, size_t len, uint64_t seed) { return tsb::xxh64(data, len, seed); }
