@@ -82,6 +82,9 @@ typedef struct tsb_dg_replay_config {
   uint32_t disk_tier, disk_prefetch, home_blocks, disk_staging;
   const uint8_t* disk;
   uint64_t* xstats;
+  /* reset_at (0 = never): ss_dg_reset_open after the boundary of token reset_at - 1, before that token's table and
+   * counters are recorded (the open placement restored, moving only misplaced units) */
+  uint32_t reset_at, reserved;
 } tsb_dg_replay_config;
 SS_API ss_status tsb_test_dg_replay(const tsb_dg_replay_config* cfg, const int32_t* ids, const int32_t* preds,
                                     int32_t* tables, uint64_t* stats, const uint8_t* src_units, uint64_t* read_sum);

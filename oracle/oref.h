@@ -31,6 +31,7 @@ typedef struct oref_dg_config {
   uint32_t disk_tier, disk_prefetch, home_blocks, disk_staging;
   const uint8_t* disk;
   uint64_t* xstats;
+  uint32_t reset_at, reserved;  /* reset_at (0 = never): reset_open after the boundary of token reset_at - 1 */
 } oref_dg_config;
 #define OREF_NXSTATS 6
 

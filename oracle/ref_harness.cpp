@@ -184,6 +184,7 @@ extern "C" __attribute__((visibility("default"))) int oref_dg_replay(const oref_
         if (core.deferred() && g + 1 < c->n_gated) core.issue_writebacks(g, [] { return false; });
       }
       core.end_token({});
+      if (c->reset_at && tok + 1 == c->reset_at) core.reset_open();
       std::memcpy(tables + size_t(tok) * keys, t.table_.data(), size_t(keys) * 4);
       const ts::DgStats& s = core.stats();
       const uint64_t v[OREF_NSTATS] = {s.tokens,          s.lookups,     s.misses,        s.covered,

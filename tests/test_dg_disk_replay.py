@@ -151,3 +151,49 @@ def test_random_file_tier_configurations_match_reference(ref, seed):
         _compare(cfg, ids, preds)
     except AssertionError as e:
         raise AssertionError("case %s: %s" % (kw, e))
+
+
+@pytest.mark.parametrize("name,kw", [
+    ("two_tier", dict(disk=False)),
+    ("two_tier_inclusive", dict(disk=False, inclusive=4, Q=8)),
+    ("files_and_pinned", dict()),
+    ("files_only", dict(pinned=0)),
+    ("file_predictions", dict(n_pred=2, disk_prefetch=1)),
+    ("deferred_on_demand_stream", dict(wb_on_d2h=0, pinned=2)),
+])
+def test_reset_open_mid_trace_matches_reference(ref, name, kw):
+    """ss_dg_reset_open between two tokens (after token 19 of 40): both caches restore the open placement, moving
+    only misplaced units (file units read back into their open slot or block, units whose open home is their file
+    dropped); the tables, counters and file counters stay identical, and every unit read through the table after the
+    reset, with real bytes, is its own."""
+    disk = kw.pop("disk", True)
+    G, U, parts = 4, 12, (256, 512, 256)
+    if disk:
+        cfg, ids, preds = make_disk_case(G=G, U=U, parts=parts, R=2, D=1, B=2, tokens=40, s=0.7, **kw)
+    else:
+        from test_dg_replay import make_case
+        cfg, ids, preds = make_case(G=G, U=U, parts=parts, R=2, D=1, B=2, tokens=40, s=0.7, **kw)
+    cfg.move_bytes = 1
+    cfg.reset_at = 20
+    unit = sum(parts)
+    src = np.random.default_rng(9).integers(0, 256, size=G * U * unit, dtype=np.uint8)
+    x_ref = np.zeros((cfg.tokens, 6), dtype=np.uint64)
+    x_new = np.zeros((cfg.tokens, 6), dtype=np.uint64)
+    t_ref, s_ref, r_ref = oracle.ref_replay(cfg, ids, preds, src_units=src, want_reads=True, xstats=x_ref)
+    t_new, s_new, r_new = runtime.replay(cfg, ids, preds, src_units=src, want_reads=True, xstats=x_new)
+    for t in range(cfg.tokens):
+        assert np.array_equal(t_new[t], t_ref[t]), "slot table differs after token %d" % t
+        assert np.array_equal(s_new[t], s_ref[t]), "counters differ after token %d" % t
+        assert np.array_equal(x_new[t], x_ref[t]), "file counters differ after token %d" % t
+    assert np.array_equal(r_new, r_ref)
+    # the table right after the reset is the open one: the same as after a reset following the first token
+    cfg.reset_at = 1
+    t_first = runtime.replay(cfg, ids, preds)[0]
+    assert np.array_equal(t_new[19], t_first[0])
+    assert not np.array_equal(t_new[18], t_new[19]), "the reset must have moved units"
+    orc = oracle.orc()
+    want = [orc.orc_checksum(src[k * unit:].ctypes.data, unit) for k in range(G * U)]
+    for t in range(cfg.tokens):
+        for g in range(G):
+            for i in range(cfg.n_ids):
+                assert r_new[t, g, i] == want[g * U + int(ids[t, g, i])], (t, g, i)

@@ -144,6 +144,7 @@ void dg_replay(const tsb_dg_replay_config* c, const int32_t* ids, const int32_t*
       if (core.deferred() && g + 1 < c->n_gated) core.issue_writebacks(g, [] { return false; });
     }
     core.end_token({});
+    if (c->reset_at && t + 1 == c->reset_at) core.reset_open();
     std::memcpy(tables + size_t(t) * keys, m.table_.data(), size_t(keys) * 4);
     const CacheStats& s = core.stats();
     const uint64_t v[16] = {s.tokens,        s.lookups,     s.misses,          s.covered,     s.fetched,
