@@ -85,6 +85,12 @@ typedef struct tsb_dg_replay_config {
   /* reset_at (0 = never): ss_dg_reset_open after the boundary of token reset_at - 1, before that token's table and
    * counters are recorded (the open placement restored, moving only misplaced units) */
   uint32_t reset_at, reserved;
+  /* scored eviction: policy 0 LRU, 1 SCORED, 2 SCORED_AUTO; rows = each token's row count at its boundary (0 = 1);
+   * weights out of 1000 (all 0 = 700 / 200 / 100); profile (optional): per gated layer units^2 transition counts,
+   * row-major [previous unit][unit], loaded as the open state */
+  uint32_t policy, rows;
+  uint32_t w_trans, w_freq, w_rec, reserved2;
+  const uint32_t* profile;
 } tsb_dg_replay_config;
 SS_API ss_status tsb_test_dg_replay(const tsb_dg_replay_config* cfg, const int32_t* ids, const int32_t* preds,
                                     int32_t* tables, uint64_t* stats, const uint8_t* src_units, uint64_t* read_sum);

@@ -32,6 +32,11 @@ typedef struct oref_dg_config {
   const uint8_t* disk;
   uint64_t* xstats;
   uint32_t reset_at, reserved;  /* reset_at (0 = never): reset_open after the boundary of token reset_at - 1 */
+  /* scored eviction: policy 0 LRU / 1 SCORED / 2 SCORED_AUTO, rows per boundary (0 = 1), weights out of 1000 (all 0 =
+   * the defaults), profile (optional): per gated layer units^2 counts, loaded through a TSSCPRF1 profile */
+  uint32_t policy, rows;
+  uint32_t w_trans, w_freq, w_rec, reserved2;
+  const uint32_t* profile;
 } oref_dg_config;
 #define OREF_NXSTATS 6
 

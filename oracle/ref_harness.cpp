@@ -11,6 +11,7 @@
 #include <vector>
 
 #include "dg_core.hpp"
+#include "dg_score.hpp"
 #include "oref.h"
 #include "xxh64.hpp"
 
@@ -141,6 +142,14 @@ extern "C" __attribute__((visibility("default"))) int oref_dg_replay(const oref_
     cfg.home_blocks = c->home_blocks;
     cfg.disk_staging = c->disk_staging;
     cfg.disk_queue = 1;  // synchronous reads
+    cfg.scored = c->policy != 0;  // the bounded boundary selection, as its device-gated context configures it
+    cfg.scored_auto = c->policy == 2;
+    cfg.boundary_score = true;
+    if (c->w_trans || c->w_freq || c->w_rec) {
+      cfg.w_trans = c->w_trans;
+      cfg.w_freq = c->w_freq;
+      cfg.w_rec = c->w_rec;
+    }
     uint32_t keys = 0;
     for (uint32_t g = 0; g < c->n_gated; ++g) keys += c->n_units[g];
     const uint32_t slots = c->persistent_slots + 2 * c->bank_slots + 1;
@@ -152,6 +161,17 @@ extern "C" __attribute__((visibility("default"))) int oref_dg_replay(const oref_
     std::vector<uint8_t> disk;
     if (cfg.disk_tier && c->disk) disk.assign(c->disk, c->disk + keys);
     core.place(order, disk.empty() ? nullptr : &disk);
+    if (c->profile && cfg.scored) {  // through the profile format: written, then checked and loaded
+      std::vector<std::vector<uint32_t>> cells(c->n_gated);
+      const uint32_t* p = c->profile;
+      for (uint32_t g = 0; g < c->n_gated; ++g) {
+        cells[g].assign(p, p + size_t(c->n_units[g]) * c->n_units[g]);
+        p += size_t(c->n_units[g]) * c->n_units[g];
+      }
+      const std::string id(32, '\x5a');
+      const std::string blob = ts::dg_profile_write(cfg.n_units, id, "replay", cells);
+      core.load_profile(blob.data(), blob.size(), id);
+    }
     t.upload_table(core.table().data(), keys);
     if (t.move_ && src_units && c->move_bytes == 1)  // the open's fill: every unit into its slot or block
       for (uint32_t k = 0; k < keys; ++k) {
@@ -182,8 +202,9 @@ extern "C" __attribute__((visibility("default"))) int oref_dg_replay(const oref_
           core.serve_prediction(g + 1, pred.data(), c->n_pred, c->n_ids, false);
         }
         if (core.deferred() && g + 1 < c->n_gated) core.issue_writebacks(g, [] { return false; });
+        core.score_layer(g);  // (the service closes each layer after its work)
       }
-      core.end_token({});
+      core.end_token({}, c->rows ? c->rows : 1);
       if (c->reset_at && tok + 1 == c->reset_at) core.reset_open();
       std::memcpy(tables + size_t(tok) * keys, t.table_.data(), size_t(keys) * 4);
       const ts::DgStats& s = core.stats();

@@ -138,7 +138,9 @@ class dg_replay_config(C.Structure):
                 ("n_order", u32), ("order", C.POINTER(u32)), ("tokens", u32), ("n_ids", u32), ("n_pred", u32),
                 ("move_bytes", u32), ("inclusive", u32), ("disk_tier", u32), ("disk_prefetch", u32),
                 ("home_blocks", u32), ("disk_staging", u32), ("disk", C.POINTER(C.c_uint8)),
-                ("xstats", C.POINTER(u64)), ("reset_at", u32), ("reserved", u32)]
+                ("xstats", C.POINTER(u64)), ("reset_at", u32), ("reserved", u32), ("policy", u32), ("rows", u32),
+                ("w_trans", u32), ("w_freq", u32), ("w_rec", u32), ("reserved2", u32),
+                ("profile", C.POINTER(u32))]
 
 
 class tsb_peer_tier(C.Structure):

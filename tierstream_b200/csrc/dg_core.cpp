@@ -27,6 +27,28 @@ SlotCache::SlotCache(const CacheConfig& cfg, Mover* m) : c_(cfg), m_(m) {
           "device-gated: file tier options without the file tier");
   require(uint64_t(c_.blocks) + c_.disk_staging < 0x7fffffffull, SS_E_INVALID, "device-gated: too many host blocks");
   stage_ev_.assign(c_.disk_staging, nullptr);
+  run_.assign(c_.n_units.size(), 1);
+  if (c_.scored) {  // every score table allocated now (the service thread never allocates)
+    require(c_.w_trans <= 1000 && c_.w_freq <= 1000 && c_.w_rec <= 1000 && c_.w_trans + c_.w_freq + c_.w_rec == 1000,
+            SS_E_INVALID, "device-gated: score weights must each be 0..1000 and sum to 1000");
+    require(c_.max_ids >= 1 && c_.max_ids <= 64, SS_E_INVALID, "device-gated: score unions need max ids 1..64");
+    sc_.resize(c_.n_units.size());
+    for (size_t g = 0; g < sc_.size(); ++g) {
+      const size_t n = c_.n_units[g];
+      require(n <= 65536, SS_E_INVALID,
+              "device-gated: scored eviction needs at most 65536 units per gated layer (gated layer " +
+                  std::to_string(g) + " has " + std::to_string(n) + ")");
+      LayerScore& l = sc_[g];
+      l.T.assign(n * n, 0);
+      l.rowsum.assign(n, 0);
+      l.cnt.assign(n, 0);
+      l.ring.assign(size_t(kWindow) * c_.max_ids, 0);
+      l.ring_len.assign(kWindow, 0);
+      l.prev.reserve(c_.max_ids);
+      l.cur.reserve(c_.max_ids);
+    }
+    select_heap_.reserve(c_.persistent_slots);
+  }
   e_.assign(keys_, Entry{});
   table_.assign(keys_, -1);
   bank_key_.assign(2u * size_t(c_.bank_slots), kNil);
@@ -152,6 +174,7 @@ void SlotCache::place(const std::vector<uint32_t>& order, const std::vector<uint
   open_hhead_ = hhead_;
   open_htail_ = htail_;
   open_on_file_ = on_file_;
+  open_stamp_ = stamp_;
 }
 
 // ---- file tier: the pinned homes' recency list (head = most recently homed; only kept with the file tier) ----
@@ -248,6 +271,16 @@ void SlotCache::push_front(uint32_t k) {
   else tail_ = k;
   head_ = k;
   x.listed = true;
+  if (c_.scored) {  // unique stamps, larger nearer the head (stamp_room keeps the counter far from wrapping)
+    if (stamp_ == UINT64_MAX) broken("the recency stamp counter wrapped");
+    x.lru_stamp = ++stamp_;
+  }
+}
+
+void SlotCache::stamp_room(const char* what) const {
+  if (c_.scored && stamp_ > kStampLimit)
+    fail(SS_E_BACKEND, std::string("device-gated: ") + what +
+                           ": the scored eviction's recency stamp counter is exhausted (reopen the context)");
 }
 
 void* SlotCache::event() {
@@ -383,7 +416,15 @@ int32_t SlotCache::bank_slot(uint32_t g) {
   return slot;
 }
 
-void SlotCache::begin_token(uint32_t seq) {
+void SlotCache::begin_token(uint32_t seq, const std::vector<uint8_t>* run) {
+  require(!run || run->size() == gated(), SS_E_INVALID, "device-gated: the exported layers do not cover the gated layers");
+  if (run) std::copy(run->begin(), run->end(), run_.begin());
+  else std::fill(run_.begin(), run_.end(), uint8_t(1));
+  if (c_.scored) {  // the token's epoch (the first is 1); one token cannot push more than 2^40 stamps
+    stamp_room("begin_token");
+    require(epoch_ < (uint64_t(1) << 63), SS_E_BACKEND, "device-gated: the scored eviction's epoch counter is exhausted");
+    ++epoch_;
+  }
   seq_ = seq;
   pf_token_ = 0;
   demand_free_used_ = 0;
@@ -560,6 +601,7 @@ void SlotCache::use(uint32_t g, uint32_t unit, bool was_miss) {
       ++st_.miss_layers;
     }
   }
+  if (c_.scored) x.demand_epoch = epoch_;  // a routed use (never a prefetch, a resurrection or a seed)
   if (x.via_pf && !x.used) {
     x.used = true;
     ++st_.prefetch_used;
@@ -600,6 +642,7 @@ void SlotCache::serve_use(uint32_t g, const uint32_t* ids, uint32_t n, uint64_t 
   uniq_.assign(ids, ids + n);
   std::sort(uniq_.begin(), uniq_.end());
   uniq_.erase(std::unique(uniq_.begin(), uniq_.end()), uniq_.end());
+  if (c_.scored) score_history(g);  // (the union saved before a prediction reuses uniq_)
   for (uint32_t id : uniq_) {
     bool miss = false;
     for (uint32_t i = 0; i < n; ++i)
@@ -631,7 +674,7 @@ void SlotCache::serve_prediction(uint32_t g_next, const uint32_t* pred, uint32_t
   for (uint32_t id : pred_) fetch(g_next, id, true);
 }
 
-void SlotCache::end_token(const std::vector<uint32_t>& keep) {
+void SlotCache::end_token(const std::vector<uint32_t>& keep, uint32_t rows) {
   m_->sync(Mover::kDem);
   m_->sync(Mover::kPf);
   std::vector<uint8_t> kept;
@@ -722,10 +765,29 @@ void SlotCache::end_token(const std::vector<uint32_t>& keep) {
     ++got;
     return true;
   };
-  for (uint32_t k = tail_; k != kNil && base + got < c_.spare_target;) {
-    const uint32_t prev = e_[k].prev;
-    if (eligible(k) && !accept(k)) break;
-    k = prev;
+  // scored eviction: the lowest scores among the eligible units, when every gated layer was closed this token (a
+  // layer the token did not export is closed here from its unchanged history); else the recency tail
+  const bool want_score = c_.scored && (!c_.scored_auto || rows > 1);
+  for (uint32_t g = 0; c_.scored && g < gated(); ++g)
+    if (!run_[g]) sc_[g].list_epoch = epoch_;
+  bool by_score = want_score;
+  for (uint32_t g = 0; by_score && g < gated(); ++g) by_score = sc_[g].list_epoch == epoch_;
+  if (want_score && !by_score) ++st_.score_fallbacks;
+  if (by_score) {
+    const auto t0 = std::chrono::steady_clock::now();
+    select_scored(c_.spare_target > base ? c_.spare_target - base : 0, eligible);
+    for (const ScoreCand& cd : select_heap_) {
+      if (!accept(cd.key)) break;
+      ++st_.scored_victims;
+    }
+    st_.score_ns += uint64_t(
+        std::chrono::duration_cast<std::chrono::nanoseconds>(std::chrono::steady_clock::now() - t0).count());
+  } else {
+    for (uint32_t k = tail_; k != kNil && base + got < c_.spare_target;) {
+      const uint32_t prev = e_[k].prev;
+      if (eligible(k) && !accept(k)) break;
+      k = prev;
+    }
   }
   if (pressure_ && pressure_recent_ && !short_blocks) {  // test pressure: the most recent ones too
     uint32_t n = 0;
@@ -770,7 +832,145 @@ void SlotCache::end_token(const std::vector<uint32_t>& keep) {
   ++st_.tokens;
 }
 
+// ---- scored eviction ----
+// Layer g's union of this token (uniq_, sorted) against the previous token's: every (r in the previous union, e in
+// this one) cell takes one saturating increment and its row sum with it; the union enters the window ring (the oldest
+// leaves it once 16 are held) and becomes the previous one.
+void SlotCache::score_history(uint32_t g) {
+  LayerScore& l = sc_[g];
+  const uint32_t n = units(g);
+  require(uniq_.size() <= c_.max_ids, SS_E_BACKEND, "device-gated: a score union above max ids");
+  l.cur.assign(uniq_.begin(), uniq_.end());
+  l.served = epoch_;
+  for (uint32_t r : l.prev) {
+    uint32_t* row = l.T.data() + size_t(r) * n;
+    for (uint32_t e : l.cur) {
+      if (row[e] == UINT32_MAX) {
+        ++st_.score_saturated;
+        continue;
+      }
+      ++row[e];
+      ++l.rowsum[r];
+    }
+  }
+  if (l.ring_n == kWindow) {
+    const uint32_t* old = l.ring.data() + size_t(l.ring_head) * c_.max_ids;
+    for (uint32_t i = 0; i < l.ring_len[l.ring_head]; ++i) --l.cnt[old[i]];
+    l.ring_head = (l.ring_head + 1) % kWindow;
+    --l.ring_n;
+  }
+  const uint32_t at = (l.ring_head + l.ring_n) % kWindow;
+  std::copy(l.cur.begin(), l.cur.end(), l.ring.begin() + ptrdiff_t(size_t(at) * c_.max_ids));
+  l.ring_len[at] = uint8_t(l.cur.size());
+  ++l.ring_n;
+  for (uint32_t e : l.cur) ++l.cnt[e];
+  l.prev.assign(l.cur.begin(), l.cur.end());
+}
+
+void SlotCache::score_layer(uint32_t g) {
+  if (!c_.scored || g >= gated() || sc_[g].served != epoch_) return;  // (not served: the boundary falls back)
+  sc_[g].list_epoch = epoch_;
+}
+
+// Unit u of layer g with cur = this token's union: N = sum over r in cur of T[r][u], D = sum over cur of the row
+// sums, P = ((|cur| N) << 16) / max(1, D), F = (cnt[u] << 16) / 16, Rec = (1 << 16) / (1 + epoch - demand_epoch),
+// S = w_t P + w_f F + w_r Rec in unsigned floor arithmetic (N <= D, so P <= |cur| << 16 and S < 2^33). With a cutoff
+// that F and Rec alone cannot beat, the transition rows are not read.
+SlotCache::ScoreCand SlotCache::score_candidate(uint32_t g, uint32_t u, uint64_t D, const ScoreCand* cutoff) const {
+  const LayerScore& l = sc_[g];
+  const Entry& x = e_[base_[g] + u];
+  const uint64_t F = (uint64_t(l.cnt[u]) << 16) / kWindow;
+  const uint64_t R = (uint64_t(1) << 16) / (1 + (epoch_ - x.demand_epoch));
+  ScoreCand cd{uint64_t(c_.w_freq) * F + uint64_t(c_.w_rec) * R, x.demand_epoch, x.lru_stamp, base_[g] + u};
+  if (cutoff && !cand_less(cd, *cutoff)) return cd;
+  uint64_t N = 0;
+  for (uint32_t r : l.cur) N += l.T[size_t(r) * units(g) + u];
+  const uint64_t P = ((uint64_t(l.cur.size()) * N) << 16) / std::max<uint64_t>(1, D);
+  cd.s += uint64_t(c_.w_trans) * P;
+  return cd;
+}
+
+// The `need` lowest candidates (cand_less) of every gated layer's eligible units, ascending in select_heap_: a bounded
+// max-heap over all layers, scored from each layer's current union, epochs and stamps.
+void SlotCache::select_scored(size_t need, const std::function<bool(uint32_t)>& eligible) {
+  select_heap_.clear();
+  for (uint32_t g = 0; need && g < gated(); ++g) {
+    uint64_t D = 0;
+    for (uint32_t r : sc_[g].cur) D += sc_[g].rowsum[r];
+    ++st_.score_layers;
+    for (uint32_t u = 0; u < units(g); ++u) {
+      if (!eligible(base_[g] + u)) continue;
+      ++st_.score_candidates;
+      const ScoreCand cd = score_candidate(g, u, D, select_heap_.size() == need ? &select_heap_.front() : nullptr);
+      if (select_heap_.size() < need) {
+        select_heap_.push_back(cd);
+        std::push_heap(select_heap_.begin(), select_heap_.end(), cand_less);
+      } else if (cand_less(cd, select_heap_.front())) {
+        std::pop_heap(select_heap_.begin(), select_heap_.end(), cand_less);
+        select_heap_.back() = cd;
+        std::push_heap(select_heap_.begin(), select_heap_.end(), cand_less);
+      }
+    }
+  }
+  std::sort_heap(select_heap_.begin(), select_heap_.end(), cand_less);
+}
+
+// The open state of every score table: the profile's counts (or zeros), an empty window, no union, epoch 0, the
+// open's stamps.
+void SlotCache::reset_score() {
+  for (uint32_t g = 0; g < uint32_t(sc_.size()); ++g) {
+    LayerScore& l = sc_[g];
+    const uint32_t n = units(g);
+    if (l.open_T.empty()) std::fill(l.T.begin(), l.T.end(), 0u);
+    else std::copy(l.open_T.begin(), l.open_T.end(), l.T.begin());
+    for (uint32_t r = 0; r < n; ++r) {
+      uint64_t sum = 0;
+      for (uint32_t e = 0; e < n && !l.open_T.empty(); ++e) sum += l.T[size_t(r) * n + e];
+      l.rowsum[r] = sum;
+    }
+    std::fill(l.cnt.begin(), l.cnt.end(), uint16_t(0));
+    std::fill(l.ring.begin(), l.ring.end(), 0u);
+    std::fill(l.ring_len.begin(), l.ring_len.end(), uint8_t(0));
+    l.ring_head = l.ring_n = 0;
+    l.prev.clear();
+    l.cur.clear();
+    l.served = l.list_epoch = 0;
+  }
+  epoch_ = 0;
+  stamp_ = open_stamp_;
+}
+
+void SlotCache::set_policy(uint32_t policy) {
+  require(policy <= 2, SS_E_INVALID, "device-gated: policy must be LRU, SCORED or SCORED_AUTO");
+  require(!policy || !sc_.empty(), SS_E_INVALID, "device-gated: scoring must be provisioned at open");
+  drain();
+  collect();
+  c_.scored = policy != 0;
+  c_.scored_auto = policy == 2;
+  reset_score();
+  for (Entry& x : e_) x.demand_epoch = x.lru_stamp = 0;
+  stamp_ = 0;
+  for (uint32_t k = tail_; k != kNil; k = e_[k].prev) e_[k].lru_stamp = ++stamp_;
+}
+
+void SlotCache::load_counts(const std::vector<std::vector<uint32_t>>& cells) {
+  require(c_.scored && cells.size() == sc_.size(), SS_E_INVALID, "device-gated: a score profile needs policy SCORED");
+  for (uint32_t g = 0; g < gated(); ++g) {
+    LayerScore& l = sc_[g];
+    const uint32_t n = units(g);
+    require(cells[g].size() == size_t(n) * n, SS_E_INVALID, "device-gated: a profile layer is not units^2 counts");
+    l.T = cells[g];
+    for (uint32_t r = 0; r < n; ++r) {
+      uint64_t sum = 0;
+      for (uint32_t e = 0; e < n; ++e) sum += l.T[size_t(r) * n + e];
+      l.rowsum[r] = sum;
+    }
+    l.open_T = l.T;  // the reset_open state
+  }
+}
+
 uint32_t SlotCache::seed(const std::vector<uint32_t>& keys) {
+  stamp_room("ss_seed");
   if (!coming_.empty()) m_->sync(Mover::kPf);
   collect();
   uint32_t n = 0;
@@ -956,6 +1156,7 @@ void SlotCache::reset_open() {
   c_ = open_c_;
   apply_wb_defer();
   std::copy(open_e_.begin(), open_e_.end(), e_.begin());
+  reset_score();  // the history's open state (a profile's counts, or none)
   backed_ = 0;  // clean copies are dropped: the open holds none
   std::copy(open_table_.begin(), open_table_.end(), table_.begin());
   free_slots_ = open_free_slots_;

@@ -25,7 +25,12 @@
 //     files; a file miss reads the unit into the next of disk_staging staging buffers (round robin, after that
 //     buffer's last copy landed) and copies it from there; pinned homes keep a recency order of their own, and a
 //     victim with no free block frees one by dropping the least recently homed pinned unit to its file, or goes to
-//     its own file when no pinned unit is left (dg_core.cpp:113-238, 769-858, 1146-1368, 1783).
+//     its own file when no pinned unit is left (dg_core.cpp:113-238, 769-858, 1146-1368, 1783);
+//   - scored eviction (the reference's SS_POLICY_SCORED / SCORED_AUTO with its boundary selection): per gated layer a
+//     transition count table between successive tokens' unions of routed ids, a frequency ring of the last 16 unions
+//     and each unit's last routed token; the boundary takes, among the same eligible units, the lowest integer scores
+//     w_t P + w_f F + w_r Rec first (ties: the older use, then the less recent unit) instead of the recency tail
+//     (dg_core.cpp:1933-2130, 1811-1826).
 #pragma once
 
 #include <cstdint>
@@ -90,6 +95,12 @@ struct CacheConfig {
   // File tier (dg_disk_tier): see the file comment. disk_prefetch: predictions may read file-homed units too.
   bool disk_tier = false, disk_prefetch = false;
   uint32_t home_blocks = 0, disk_staging = 0;
+  // Scored eviction: the history is kept from the open when `scored` (the tables exist only then); scored_auto takes
+  // scored victims only after a boundary of more than one row. Weights out of 1000 (sum 1000); max_ids = the most ids
+  // one export holds (a union's bound).
+  bool scored = false, scored_auto = false;
+  uint32_t w_trans = 700, w_freq = 200, w_rec = 100;
+  uint32_t max_ids = 64;
 };
 
 struct CacheStats {
@@ -105,6 +116,10 @@ struct CacheStats {
   // buffer's last copy; pinned units dropped to their file to free a block; victims dropped to their file
   uint64_t disk_reads = 0, disk_read_bytes = 0, disk_read_ns = 0, disk_stage_waits = 0, disk_drops = 0;
   uint64_t disk_discards = 0;
+  // scored eviction: boundaries that fell back to the recency order (a layer without this token's ranking), victims
+  // taken by score, layers scored and the candidates they ranked, saturated transition increments, selection time
+  uint64_t score_fallbacks = 0, scored_victims = 0, score_layers = 0, score_candidates = 0, score_saturated = 0;
+  uint64_t score_ns = 0;
 };
 
 struct LayerCounts {
@@ -154,7 +169,9 @@ class SlotCache {
   std::vector<uint32_t> residency() const;
 
   // ---- inside a token (the service thread) ----
-  void begin_token(uint32_t seq);
+  // run (optional, one flag per gated layer): the layers this token exports (scored eviction ranks the others at the
+  // boundary from their unchanged history).
+  void begin_token(uint32_t seq, const std::vector<uint8_t>* run = nullptr);
   void serve_demand(uint32_t g, const uint32_t* ids, uint32_t n, uint64_t mask);
   void serve_use(uint32_t g, const uint32_t* ids, uint32_t n, uint64_t mask);
   void serve_prediction(uint32_t g_next, const uint32_t* pred, uint32_t n, bool ahead);
@@ -163,7 +180,19 @@ class SlotCache {
   void issue_writebacks(uint32_t g, const std::function<bool()>& ahead);
 
   // ---- between tokens (the engine thread) ----
-  void end_token(const std::vector<uint32_t>& keep);
+  // rows: the token's rows (scored_auto takes scored victims only above 1).
+  void end_token(const std::vector<uint32_t>& keep, uint32_t rows = 1);
+  // Scored eviction: gated layer g is closed for this token (its union, epochs and stamps are final); the service
+  // calls it after each served layer.
+  void score_layer(uint32_t g);
+  // Between tokens: LRU (0), SCORED (1) or SCORED_AUTO (2); the history restarts and the recency stamps follow the
+  // current recency order. Scoring must have been set up at the open (scored).
+  void set_policy(uint32_t policy);
+  bool scored() const { return c_.scored; }
+  bool scoring_ready() const { return !sc_.empty(); }
+  // A score profile's transition counts (units(g)^2 per gated layer, row-major [previous unit][unit]) as the open
+  // state of the tables (scored only; kept for reset_open).
+  void load_counts(const std::vector<std::vector<uint32_t>>& cells);
   uint32_t seed(const std::vector<uint32_t>& keys);
   void drain();
   // Restores the open placement, moving only misplaced units; `plan` receives the slot-to-slot moves in execution
@@ -187,6 +216,7 @@ class SlotCache {
     bool backed = false;  // a device unit whose block still holds its bytes (inclusive share)
     bool in_hlist = false;           // file tier: in the pinned homes' recency list
     uint32_t hprev = kNil, hnext = kNil;
+    uint64_t demand_epoch = 0, lru_stamp = 0;  // scored: the last token that routed it; its recency list position
     void* pf_done = nullptr;
   };
   struct Writeback {
@@ -205,6 +235,33 @@ class SlotCache {
 
   void unlink(uint32_t k);
   void push_front(uint32_t k);
+  // ---- scored eviction ----
+  struct ScoreCand {
+    uint64_t s, epoch, stamp;
+    uint32_t key;
+  };
+  struct LayerScore {
+    std::vector<uint32_t> T, open_T;  // transition counts [r][e]; open_T: a profile's (empty = zeros)
+    std::vector<uint64_t> rowsum;
+    std::vector<uint16_t> cnt;        // unions of the window holding each unit
+    std::vector<uint32_t> ring;       // kWindow unions of at most max_ids ids
+    std::vector<uint8_t> ring_len;
+    uint32_t ring_head = 0, ring_n = 0;
+    std::vector<uint32_t> prev, cur;  // the previous and this token's sorted unions
+    uint64_t served = 0, list_epoch = 0;
+  };
+  static constexpr uint32_t kWindow = 16;
+  static constexpr uint64_t kStampLimit = UINT64_MAX - (uint64_t(1) << 40);
+  static bool cand_less(const ScoreCand& a, const ScoreCand& b) {
+    if (a.s != b.s) return a.s < b.s;
+    if (a.epoch != b.epoch) return a.epoch < b.epoch;
+    return a.stamp < b.stamp;
+  }
+  void score_history(uint32_t g);
+  ScoreCand score_candidate(uint32_t g, uint32_t u, uint64_t denominator, const ScoreCand* cutoff) const;
+  void select_scored(size_t need, const std::function<bool(uint32_t)>& eligible);
+  void reset_score();
+  void stamp_room(const char* what) const;
   void* event();
   uint32_t collect();
   void submit_part(Deferred& d);
@@ -236,6 +293,10 @@ class SlotCache {
   uint32_t hhead_ = kNil, htail_ = kNil, on_file_ = 0, open_hhead_ = kNil, open_htail_ = kNil, open_on_file_ = 0;
   uint32_t stage_next_ = 0;
   std::vector<void*> stage_ev_;  // per staging buffer: its last copy's event
+  std::vector<LayerScore> sc_;
+  std::vector<uint8_t> run_;
+  uint64_t epoch_ = 0, stamp_ = 0, open_stamp_ = 0;
+  std::vector<ScoreCand> select_heap_;
   std::deque<Writeback> wbs_;
   std::deque<Deferred> deferred_;
   Mover::Stream wb_stream_ = Mover::kDem;

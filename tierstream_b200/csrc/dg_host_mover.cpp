@@ -102,6 +102,15 @@ void dg_replay(const tsb_dg_replay_config* c, const int32_t* ids, const int32_t*
   cfg.disk_prefetch = c->disk_prefetch != 0;
   cfg.home_blocks = c->home_blocks;
   cfg.disk_staging = c->disk_staging;
+  require(c->policy <= 2, SS_E_INVALID, "tsb_test_dg_replay: policy 0..2");
+  cfg.scored = c->policy != 0;
+  cfg.scored_auto = c->policy == 2;
+  if (c->w_trans || c->w_freq || c->w_rec) {
+    cfg.w_trans = c->w_trans;
+    cfg.w_freq = c->w_freq;
+    cfg.w_rec = c->w_rec;
+  }
+  cfg.max_ids = c->n_ids;
   uint32_t keys = 0;
   for (uint32_t g = 0; g < c->n_gated; ++g) keys += c->n_units[g];
   HostMover m(std::vector<uint64_t>(c->part_bytes, c->part_bytes + c->n_parts), keys,
@@ -112,6 +121,15 @@ void dg_replay(const tsb_dg_replay_config* c, const int32_t* ids, const int32_t*
   std::vector<uint8_t> disk;
   if (cfg.disk_tier && c->disk) disk.assign(c->disk, c->disk + keys);
   core.place(order, disk.empty() ? nullptr : &disk);
+  if (c->profile && cfg.scored) {
+    std::vector<std::vector<uint32_t>> cells(c->n_gated);
+    const uint32_t* p = c->profile;
+    for (uint32_t g = 0; g < c->n_gated; ++g) {
+      cells[g].assign(p, p + size_t(c->n_units[g]) * c->n_units[g]);
+      p += size_t(c->n_units[g]) * c->n_units[g];
+    }
+    core.load_counts(cells);
+  }
   m.upload_table(core.table().data(), keys);
   if (m.move_ && src_units)  // the open's fill: every unit with a slot or a block (a file home stays in its file)
     for (uint32_t k = 0; k < keys; ++k) {
@@ -142,8 +160,9 @@ void dg_replay(const tsb_dg_replay_config* c, const int32_t* ids, const int32_t*
         core.serve_prediction(g + 1, pred.data(), c->n_pred, false);
       }
       if (core.deferred() && g + 1 < c->n_gated) core.issue_writebacks(g, [] { return false; });
+      core.score_layer(g);
     }
-    core.end_token({});
+    core.end_token({}, c->rows ? c->rows : 1);
     if (c->reset_at && t + 1 == c->reset_at) core.reset_open();
     std::memcpy(tables + size_t(t) * keys, m.table_.data(), size_t(keys) * 4);
     const CacheStats& s = core.stats();

@@ -241,9 +241,11 @@ class TokenGraph:
 def replay_config(n_units, part_bytes, persistent_slots, bank_slots, blocks, spare_target, order, tokens, n_ids,
                   n_pred=0, prefetch_reserve=0xFFFFFFFF, prefetch_per_layer=4, prefetch_per_token=48, wb_defer=1,
                   wb_on_d2h=1, wb_layer_bytes=0, wb_max_outstanding=0, move_bytes=0, inclusive=0, disk=None,
-                  home_blocks=0, disk_staging=0, disk_prefetch=0):
+                  home_blocks=0, disk_staging=0, disk_prefetch=0, policy=0, rows=1, weights=None, profile=None):
     """A dg_replay_config with its arrays kept alive on the returned object. disk (file tier): one flag per key for
-    the plan's disk units (blocks then counts home_blocks + the spare blocks); xstats is attached by replay()."""
+    the plan's disk units (blocks then counts home_blocks + the spare blocks); xstats is attached by replay().
+    policy (scored eviction): 0 LRU, 1 SCORED, 2 SCORED_AUTO, with each boundary's row count `rows`, weights
+    (w_trans, w_freq, w_rec) out of 1000 and an optional profile: per gated layer units x units transition counts."""
     c = abi.dg_replay_config()
     keep = {}
     keep["n_units"] = (C.c_uint32 * len(n_units))(*n_units)
@@ -261,6 +263,13 @@ def replay_config(n_units, part_bytes, persistent_slots, bank_slots, blocks, spa
     c.n_order = len(order)
     c.order = keep["order"]
     c.tokens, c.n_ids, c.n_pred, c.move_bytes, c.inclusive = tokens, n_ids, n_pred, move_bytes, inclusive
+    c.policy, c.rows = policy, rows
+    if weights:
+        c.w_trans, c.w_freq, c.w_rec = weights
+    if profile is not None:
+        flat = np.ascontiguousarray(np.concatenate([np.asarray(x, dtype=np.uint32).reshape(-1) for x in profile]))
+        keep["profile"] = flat
+        c.profile = flat.ctypes.data_as(C.POINTER(C.c_uint32))
     if disk is not None:
         keep["disk"] = (C.c_uint8 * max(1, len(disk)))(*[1 if f else 0 for f in disk])
         c.disk_tier, c.disk_prefetch, c.home_blocks, c.disk_staging = 1, disk_prefetch, home_blocks, disk_staging
