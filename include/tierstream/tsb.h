@@ -110,6 +110,14 @@ SS_API ss_status tsb_test_host_locs(ss_ctx* c, int layer, int32_t* out, int n);
 SS_API ss_status tsb_test_file_read(const char* path, uint64_t offset, uint64_t bytes, void* dst, uint64_t piece,
                                     uint32_t threads, int direct);
 
+/* Test hooks of scored eviction's profile (the reference's TSSCPRF1 format, ss.h "Scored eviction"): the SHA-256 of
+ * len bytes into out[32]; the profile identity of d's gated layers (every layer with units) into identity[32] and,
+ * when profile is given, every rule of the format checked (SS_E_INVALID naming the first one broken) and its counts
+ * copied into cells (at most cells_cap). */
+SS_API ss_status tsb_test_sha256(const void* data, uint64_t len, uint8_t* out);
+SS_API ss_status tsb_test_score_profile(const ss_desc* d, const void* profile, uint64_t len, uint8_t* identity,
+                                        uint32_t* cells, uint64_t cells_cap);
+
 /* ---- Host xxh64 (this library's, the one the open's fill checks pinned units with; seed 0 in the descriptor) ---- */
 SS_API uint64_t tsb_xxh64(const void* data, size_t len, uint64_t seed);
 

@@ -15,6 +15,7 @@ SS_OK, SS_E_INVALID, SS_E_DESC, SS_E_IO, SS_E_NOMEM, SS_E_BACKEND, SS_E_CAPACITY
 STATUS_NAMES = ["SS_OK", "SS_E_INVALID", "SS_E_DESC", "SS_E_IO", "SS_E_NOMEM", "SS_E_BACKEND", "SS_E_CAPACITY",
                 "SS_E_HASH", "SS_E_UNSUPPORTED", "SS_E_RECIPE"]
 SS_TIER_RESIDENT, SS_TIER_PINNED, SS_TIER_DISK, SS_TIER_PAIR, SS_TIER_RESIDENT_BACKED = range(5)
+SS_POLICY_LRU, SS_POLICY_SCORED, SS_POLICY_SCORED_AUTO = range(3)
 SS_TIER_MODE_INCLUSIVE, SS_TIER_MODE_EXCLUSIVE = 0, 1
 SS_BACKEND_CPU, SS_BACKEND_CUDA, SS_BACKEND_HIP = 0, 1, 2
 SS_FORWARD_HOST, SS_FORWARD_DEVICE_GATED = 0, 1
@@ -210,6 +211,7 @@ _PROTOS = {
     "ss_dg_timeline_sized": (C.c_int, [vp, C.c_int, P(ss_dg_layer_timeline), u32]),
     "ss_dg_boundary_timeline_sized": (C.c_int, [vp, P(ss_dg_boundary_timeline), u32]),
     "ss_dg_reset_open": (C.c_int, [vp]),
+    "ss_dg_set_policy": (C.c_int, [vp, C.c_int]),
     "ss_test_dg_check": (C.c_int, [vp]),
     "ss_test_dg_flags": (C.c_int, [vp, u32]),
     "ss_test_dg_pressure": (C.c_int, [vp, u32, u32]),
@@ -219,6 +221,8 @@ _PROTOS = {
     "tsb_move": (C.c_int, [P(vp), P(vp), P(u64), u32, vp, P(u32), P(i32), u32, vp, u32, vp, u32, vp]),
     "tsb_move_timeouts": (C.c_int, []),
     "tsb_test_file_read": (C.c_int, [C.c_char_p, u64, u64, vp, u64, u32, C.c_int]),
+    "tsb_test_sha256": (C.c_int, [vp, u64, vp]),
+    "tsb_test_score_profile": (C.c_int, [vp, vp, u64, vp, vp, u64]),
     "tsb_xxh64_units": (C.c_int, [P(vp), P(u64), P(u32), u32, vp, vp, vp, vp, vp]),
     "tsb_xxh64_units_static": (C.c_int, [P(vp), P(u64), P(u32), u32, vp, vp, vp, vp]),
     "tsb_peer_plan": (C.c_int, [P(u64), u32, u32, P(u64), P(C.c_int32)]),

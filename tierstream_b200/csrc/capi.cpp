@@ -14,6 +14,7 @@
 #include "json.hpp"
 #include "peer.hpp"
 #include "plan.hpp"
+#include "score_profile.hpp"
 #include "strix_stream/ss.h"
 #include "strix_stream/ss_test.h"
 #include "tierstream/tsb.h"
@@ -424,7 +425,7 @@ ss_status ss_release(ss_ctx* c, int layer, void* s) {
 }
 ss_status ss_end(ss_ctx* c) {
   return ctx_guard(c, [&] {
-    if (c->dg) c->dg->end();
+    if (c->dg) c->dg->end(1);
     else c->host->end();
   });
 }
@@ -590,13 +591,12 @@ ss_status ss_dg_reset_open(ss_ctx* c) {
 ss_status ss_dg_end_rows(ss_ctx* c, uint32_t rows) {
   return ctx_guard(c, [&] {
     need(rows > 0, "ss_dg_end_rows: rows must be positive");
-    dg_of(c, "ss_dg_end_rows").end();
+    dg_of(c, "ss_dg_end_rows").end(rows);
   });
 }
 ss_status ss_dg_set_policy(ss_ctx* c, ss_policy policy) {
   return ctx_guard(c, [&] {
-    dg_of(c, "ss_dg_set_policy");
-    tsb::require(policy == SS_POLICY_LRU, SS_E_INVALID, "ss_dg_set_policy: this build has the LRU policy only");
+    dg_of(c, "ss_dg_set_policy").set_policy(uint32_t(policy));
   });
 }
 
@@ -658,6 +658,38 @@ ss_status tsb_peer_index(const int32_t* owner, uint32_t keys, uint32_t world, in
     const std::vector<int64_t> ix = tsb::store_index(std::vector<int32_t>(owner, owner + keys), world, &per);
     if (index) std::copy(ix.begin(), ix.end(), index);
     if (units_per_rank) std::copy(per.begin(), per.end(), units_per_rank);
+  });
+}
+
+ss_status tsb_test_sha256(const void* data, uint64_t len, uint8_t* out) {
+  return guard([&] {
+    need((data || !len) && out, "tsb_test_sha256: null argument");
+    const std::string h = tsb::sha256(data, size_t(len));
+    std::memcpy(out, h.data(), 32);
+  });
+}
+
+ss_status tsb_test_score_profile(const ss_desc* d, const void* profile, uint64_t len, uint8_t* identity,
+                                 uint32_t* cells, uint64_t cells_cap) {
+  return guard([&] {
+    need(d && identity, "tsb_test_score_profile: null argument");
+    std::vector<int> gated;
+    std::vector<uint32_t> units;
+    for (size_t L = 0; L < d->d.layers.size(); ++L)
+      if (d->d.layers[L].n_units > 0) {
+        gated.push_back(int(L));
+        units.push_back(uint32_t(d->d.layers[L].n_units));
+      }
+    const std::string id = tsb::score_identity(d->d, gated);
+    std::memcpy(identity, id.data(), 32);
+    if (!profile && !len) return;
+    const tsb::ScoreProfile p = tsb::check_score_profile(profile, len, units, id);
+    uint64_t at = 0;
+    for (const auto& layer : p.cells)
+      for (uint32_t v : layer) {
+        if (cells && at < cells_cap) cells[at] = v;
+        ++at;
+      }
   });
 }
 

@@ -38,7 +38,10 @@ class DgContext {
   virtual bool source_direct(int i) const = 0;
   virtual int gated_index(int layer) const = 0;
   virtual void begin(const uint32_t* rows, int n_layers) = 0;
-  virtual void end() = 0;
+  // rows: the token's rows (scored eviction's SCORED_AUTO takes scored victims only above 1)
+  virtual void end(uint32_t rows) = 0;
+  // Between tokens: LRU, SCORED or SCORED_AUTO (scoring must have been set up at the open)
+  virtual void set_policy(uint32_t policy) = 0;
   virtual void seed(int layer, const int32_t* units, int n) = 0;
   virtual void check_unit(int layer, int unit) = 0;
   virtual void device_view(ss_dg_device_view* v) const = 0;

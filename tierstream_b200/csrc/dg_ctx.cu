@@ -31,6 +31,7 @@
 #include "kernels.hpp"
 #include "peer.hpp"
 #include "pinned.hpp"
+#include "score_profile.hpp"
 #include "source_file.hpp"
 #include "xxh64.hpp"
 
@@ -106,6 +107,11 @@ struct Layout {
   bool disk_tier = false, disk_prefetch = false;
   uint32_t F = 0, S = 0;
   std::vector<uint8_t> disk;
+  // scored eviction (SS_POLICY_SCORED / SCORED_AUTO): the weights and a profile's counts (empty: none)
+  bool scored = false, scored_auto = false;
+  uint32_t w_trans = 700, w_freq = 200, w_rec = 100;
+  std::vector<std::vector<uint32_t>> profile;
+  std::string provenance;
 };
 
 Layout make_layout(const Desc& d, const Plan& p, const ss_options& o, const PeerTier* peer) {
@@ -113,9 +119,10 @@ Layout make_layout(const Desc& d, const Plan& p, const ss_options& o, const Peer
   const ss_budget& b = p.budget;
   if (b.tier_mode != SS_TIER_MODE_EXCLUSIVE) refuse(SS_E_INVALID, "needs tier_mode EXCLUSIVE");
   if (b.pinned_backing) refuse(SS_E_INVALID, "pinned_backing is refused (each unit has one home)");
-  if (o.policy == SS_POLICY_SCORED || o.policy == SS_POLICY_SCORED_AUTO)
-    refuse(SS_E_UNSUPPORTED, "scored eviction is not in this build (use SS_POLICY_LRU)");
-  if (o.policy != SS_POLICY_LRU) refuse(SS_E_INVALID, "policy must be LRU");
+  if (o.policy != SS_POLICY_LRU && o.policy != SS_POLICY_SCORED && o.policy != SS_POLICY_SCORED_AUTO)
+    refuse(SS_E_INVALID, "policy must be LRU, SCORED or SCORED_AUTO");
+  if ((o.dg_score_profile_len || o.dg_score_profile) && o.policy == SS_POLICY_LRU)
+    refuse(SS_E_INVALID, "dg_score_profile needs policy SCORED");
   if (o.pin_planned) refuse(SS_E_INVALID, "needs pin_planned = 0 (planned residents are a warm start)");
   if (!o.fill_residents) refuse(SS_E_INVALID, "needs fill_residents = 1 (a resident's slot is its only copy)");
   if (o.readahead_units) refuse(SS_E_INVALID, "readahead_units must be 0 (no gated unit is read from its file)");
@@ -136,7 +143,7 @@ Layout make_layout(const Desc& d, const Plan& p, const ss_options& o, const Peer
                              "(one read at a time inside its fetch)");
   if (o.dg_disk_tier && peer) refuse(SS_E_UNSUPPORTED, "the file tier with the peer tier is not in this build");
   if (o.dg_no_admit || o.dg_clean_evict || o.dg_pf_revert_unused || o.dg_pf_strict_admit || o.dg_landing_blocks ||
-      o.dg_bank_keep || o.dg_disk_queue_adapt || o.dg_prior_len || o.dg_score_profile_len)
+      o.dg_bank_keep || o.dg_disk_queue_adapt || o.dg_prior_len)
     refuse(SS_E_UNSUPPORTED, "an opt-in device-gated policy of the reference that is not in this build is set");
   Layout x;
   x.B = o.dg_max_ids;
@@ -202,6 +209,35 @@ Layout make_layout(const Desc& d, const Plan& p, const ss_options& o, const Peer
   x.disk_tier = o.dg_disk_tier != 0;
   x.disk_prefetch = o.dg_disk_prefetch != 0;
   x.S = x.disk_tier ? (o.dg_disk_staging ? o.dg_disk_staging : 8u) : 0u;
+  // scored eviction: the weights, the per-layer bound and the profile (every rule of its format, against this
+  // descriptor's identity), as the reference resolves them (dg_layout.cpp:349-371)
+  if (o.policy == SS_POLICY_SCORED || o.policy == SS_POLICY_SCORED_AUTO) {
+    x.scored = true;
+    x.scored_auto = o.policy == SS_POLICY_SCORED_AUTO;
+    if (o.dg_score_w_trans || o.dg_score_w_freq || o.dg_score_w_recency) {
+      if (o.dg_score_w_trans > 1000 || o.dg_score_w_freq > 1000 || o.dg_score_w_recency > 1000 ||
+          o.dg_score_w_trans + o.dg_score_w_freq + o.dg_score_w_recency != 1000)
+        refuse(SS_E_INVALID, "dg_score_w_trans / _freq / _recency must each be 0..1000 and sum to 1000");
+      x.w_trans = o.dg_score_w_trans;
+      x.w_freq = o.dg_score_w_freq;
+      x.w_rec = o.dg_score_w_recency;
+    }
+    std::vector<uint32_t> units;
+    for (int L : x.gated) {
+      units.push_back(uint32_t(d.layers[size_t(L)].n_units));
+      if (units.back() > 65536)
+        refuse(SS_E_INVALID, "scored eviction needs at most 65536 units per gated layer (layer " +
+                                 std::to_string(d.layers[size_t(L)].index) + ")");
+    }
+    if (o.dg_score_profile_len || o.dg_score_profile) {
+      if (!o.dg_score_profile || !o.dg_score_profile_len)
+        refuse(SS_E_INVALID, "dg_score_profile and dg_score_profile_len must be given together");
+      ScoreProfile prof = check_score_profile(o.dg_score_profile, o.dg_score_profile_len, units,
+                                              score_identity(d, x.gated));
+      x.profile = std::move(prof.cells);
+      x.provenance = std::move(prof.provenance);
+    }
+  }
   if (o.dg_spare_slots) {
     if (o.dg_spare_slots > x.P + x.F)
       refuse(SS_E_INVALID, "dg_spare_slots " + std::to_string(o.dg_spare_slots) + " above the non-resident units (" +
@@ -656,7 +692,7 @@ class Service {
   void serve_token(uint32_t seq) {
     const uint32_t G = core_->gated();
     std::copy(run_next_.begin(), run_next_.end(), run_.begin());
-    core_->begin_token(seq);
+    core_->begin_token(seq, &run_);
     if (diag_) std::fill(times_.begin(), times_.end(), LayerTimes{});
     wait_began(seq);
     auto t_prev = Clock::now();
@@ -701,6 +737,7 @@ class Service {
       }
       if (core_->deferred() && nx < G)
         core_->issue_writebacks(g, [&] { return !deterministic_ && load_acquire(&m_.flag[nx]) == seq; });
+      core_->score_layer(g);  // scored eviction: layer g's union, epochs and stamps are final for this token
       const auto t_end = Clock::now();
       t.serve_us = us_between(t_seen, t_end);
       if (diag_) {
@@ -817,7 +854,7 @@ class CudaDgContext final : public DgContext {
     svc_->begin(seq_, run_);
   }
 
-  void end() override {
+  void end(uint32_t rows) override {
     require(in_token_, SS_E_INVALID, "ss_end: no gated token is open");
     in_token_ = false;
     const auto deadline = Clock::now() + std::chrono::milliseconds(uint64_t(o_.dg_wait_timeout_ms) + 5000);
@@ -860,7 +897,7 @@ class CudaDgContext final : public DgContext {
       fail(SS_E_BACKEND, token_failure(dev, ""));
     }
     const auto t0 = Clock::now();
-    core_->end_token(keep_all());
+    core_->end_token(keep_all(), rows);
     boundary_.writebacks = uint32_t(core_->stats().evicted - evicted_before_);
     evicted_before_ = core_->stats().evicted;
     boundary_.sync_us = 0;
@@ -1092,6 +1129,12 @@ class CudaDgContext final : public DgContext {
     s.disk_discards = d(c.disk_discards, base_.disk_discards);
     s.disk_units = core_->file_units();
     s.disk_max_in_flight = c.disk_reads ? 1 : 0;  // (a gauge since open: one read at a time)
+    s.score_fallbacks = d(c.score_fallbacks, base_.score_fallbacks);
+    s.scored_victims = d(c.scored_victims, base_.scored_victims);
+    s.score_layers = d(c.score_layers, base_.score_layers);
+    s.score_candidates = d(c.score_candidates, base_.score_candidates);
+    s.score_saturated = d(c.score_saturated, base_.score_saturated);
+    s.score_ns = d(c.score_ns, base_.score_ns);
     s.disk_queue_resolved = x_.disk_tier ? 1u : 0u;
     std::memcpy(out, &s, sizeof s);
   }
@@ -1183,6 +1226,14 @@ class CudaDgContext final : public DgContext {
     base_ = core_->stats();
     lbase_ = core_->layer_counts();
     timeline_valid_ = false;
+  }
+
+  void set_policy(uint32_t policy) override {
+    require(!in_token_, SS_E_INVALID, "ss_dg_set_policy: between tokens only");
+    require(policy <= 2, SS_E_INVALID, "ss_dg_set_policy: policy must be LRU, SCORED or SCORED_AUTO");
+    require(!policy || core_->scoring_ready(), SS_E_INVALID,
+            "ss_dg_set_policy: scored eviction must be set up at ss_open (policy SCORED or SCORED_AUTO)");
+    core_->set_policy(policy);
   }
 
   void test_mutate(int m) override {
@@ -1430,6 +1481,12 @@ class CudaDgContext final : public DgContext {
     c.disk_prefetch = x_.disk_prefetch;
     c.home_blocks = x_.disk_tier ? x_.P : 0;  // the plan's pinned units get the blocks; the rest are spares
     c.disk_staging = x_.S;
+    c.scored = x_.scored;
+    c.scored_auto = x_.scored_auto;
+    c.w_trans = x_.w_trans;
+    c.w_freq = x_.w_freq;
+    c.w_rec = x_.w_rec;
+    c.max_ids = x_.B;
     if (x_.disk_tier) {  // a file miss: the unit's parts from their files, checked against the descriptor's hash
       unsigned n = 8;
       if (const char* e = std::getenv("TSB_FILE_READERS")) n = unsigned(std::max(1L, std::min(64L, std::atol(e))));
@@ -1456,6 +1513,7 @@ class CudaDgContext final : public DgContext {
     order.insert(order.end(), x_.residents.begin(), x_.residents.end());
     for (uint32_t k = 0; k < x_.keys; ++k) order.push_back(k);
     core_->place(order, x_.disk_tier ? &x_.disk : nullptr);
+    if (!x_.profile.empty()) core_->load_counts(x_.profile);
     open_alloc_s_ = std::chrono::duration<double>(Clock::now() - t_start).count();
     fill();
     mover_->upload_table(core_->table().data(), x_.keys);

@@ -16,7 +16,8 @@ class DgRun:
     def __init__(self, model, residents_per_layer=None, resident_keys=None, spare_per_layer=1, max_ids=2,
                  host_spare_units=None, diag=False, test_hooks=True, wb_defer=1, wb_stream=1, verify=False,
                  n_pred=0, slices=64, mode=0, timeout_ms=10000, device_bytes=None, with_reader=True,
-                 resident_order=None, inclusive=0, peer=None, disk_keys=(), disk_staging=0, disk_prefetch=0):
+                 resident_order=None, inclusive=0, peer=None, disk_keys=(), disk_staging=0, disk_prefetch=0,
+                 policy=0, weights=None, profile=None):
         self.model = model
         G, U = model.layers, model.units
         self.G, self.U, self.n_ids, self.n_pred = G, U, max_ids, n_pred
@@ -58,6 +59,13 @@ class DgRun:
         o.verify_hash = 1 if verify else 0
         o.dg_wait_timeout_ms = timeout_ms
         o.dg_inclusive_blocks = inclusive
+        o.policy = policy  # scored eviction: SS_POLICY_SCORED / SCORED_AUTO, weights out of 1000, a profile's bytes
+        if weights:
+            o.dg_score_w_trans, o.dg_score_w_freq, o.dg_score_w_recency = weights
+        if profile is not None:
+            self._profile = C.create_string_buffer(bytes(profile), len(profile))
+            o.dg_score_profile = C.addressof(self._profile)
+            o.dg_score_profile_len = len(profile)
         if self.disk_keys:
             o.dg_disk_tier = 1
             o.dg_disk_staging = disk_staging

@@ -131,6 +131,10 @@ class DgContext:
     def reset_open(self):
         abi.check(abi.load().ss_dg_reset_open(self.h))
 
+    def set_policy(self, policy):
+        """Between tokens: SS_POLICY_LRU / SCORED / SCORED_AUTO (ss_dg_set_policy)."""
+        abi.check(abi.load().ss_dg_set_policy(self.h, policy))
+
     def retier(self, tier):
         """Between tokens: the peer tier's owners and store addresses replaced (tsb_dg_peer_retier)."""
         t = tier.struct()
