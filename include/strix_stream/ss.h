@@ -515,8 +515,27 @@ SS_API ss_status ss_budget_ledger_observe(ss_budget_ledger* l, const char* stage
 SS_API int ss_budget_ledger_within_caps(const ss_budget_ledger* l);
 SS_API ss_status ss_budget_in_dg_library(ss_budget_in* in, const ss_desc* d, const ss_options* o);
 
-typedef struct ss_dg_round_params ss_dg_round_params;
-typedef struct ss_dg_round_result ss_dg_round_result;
+/* Placement rounds (device-gated, between tokens on the engine thread): every gated unit keeps a decayed count of the
+ * steps that routed it (s = decay x s + hits since the last round); a round moves units toward the placement that
+ * count ranks (the hottest on the device, the next pinned, the rest in their files), at most max_units promotions and
+ * budget_bytes bytes (0 = no limit), a unit replacing another only when its count is above hysteresis x the other's.
+ * Kept units and units with a write-back in flight never move. ss_dg_round_cancel (any thread) stops a running round
+ * at its next unit; ss_dg_round_seed_counts sets counts (finite, >= 0). */
+typedef struct ss_dg_round_params {
+  uint32_t struct_size;  /* sizeof, set by ss_dg_round_defaults */
+  uint32_t flags;        /* 0 */
+  uint64_t budget_bytes; /* 0 = no limit */
+  uint32_t max_units;    /* promotions per round (default 96) */
+  float hysteresis;      /* >= 1 (default 1.25) */
+  float decay;           /* 0..1 (default 0.85) */
+  uint32_t reserved0;
+} ss_dg_round_params;
+typedef struct ss_dg_round_result {
+  uint32_t struct_size;
+  uint32_t promoted_to_device, promoted_to_pinned, demoted_from_device, dropped_to_file;
+  uint32_t cancelled;    /* 1: stopped by ss_dg_round_cancel at a unit boundary */
+  uint64_t bytes_read, bytes_h2d, bytes_written_back, ns;
+} ss_dg_round_result;
 SS_API ss_status ss_dg_make_resident(ss_ctx* c, int g, const int32_t* ids, int n);
 SS_API void ss_dg_round_defaults_sized(ss_dg_round_params* p, uint32_t size);
 SS_API ss_status ss_dg_round_sized(ss_ctx* c, const ss_dg_round_params* p, ss_dg_round_result* out, uint32_t size);

@@ -91,6 +91,13 @@ typedef struct tsb_dg_replay_config {
   uint32_t policy, rows;
   uint32_t w_trans, w_freq, w_rec, reserved2;
   const uint32_t* profile;
+  /* placement rounds: after the boundary of every round_every-th token (0 = never), one round with these limits;
+   * rstats (optional): [tokens][6] rounds, promoted to the device, promoted to pinned, demoted from the device,
+   * dropped to their file, bytes moved, summed over the rounds so far */
+  uint32_t round_every, round_max_units;
+  float round_hysteresis, round_decay;
+  uint64_t round_budget;
+  uint64_t* rstats;
 } tsb_dg_replay_config;
 SS_API ss_status tsb_test_dg_replay(const tsb_dg_replay_config* cfg, const int32_t* ids, const int32_t* preds,
                                     int32_t* tables, uint64_t* stats, const uint8_t* src_units, uint64_t* read_sum);

@@ -37,6 +37,12 @@ typedef struct oref_dg_config {
   uint32_t policy, rows;
   uint32_t w_trans, w_freq, w_rec, reserved2;
   const uint32_t* profile;
+  /* placement rounds after the boundary of every round_every-th token (0 = never); rstats (optional): [tokens][6]
+   * rounds, promoted to device, promoted to pinned, demoted, dropped to file, bytes, summed so far */
+  uint32_t round_every, round_max_units;
+  float round_hysteresis, round_decay;
+  uint64_t round_budget;
+  uint64_t* rstats;
 } oref_dg_config;
 #define OREF_NXSTATS 6
 

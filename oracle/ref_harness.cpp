@@ -180,6 +180,7 @@ extern "C" __attribute__((visibility("default"))) int oref_dg_replay(const oref_
         std::memcpy(dst, src_units + size_t(k) * t.unit_, t.unit_);
       }
     std::vector<uint32_t> row(c->n_ids), pred(c->n_pred);
+    uint64_t rsum[6] = {0, 0, 0, 0, 0, 0};
     for (uint32_t tok = 0; tok < c->tokens; ++tok) {
       core.begin_token(tok + 1);
       for (uint32_t g = 0; g < c->n_gated; ++g) {
@@ -206,6 +207,21 @@ extern "C" __attribute__((visibility("default"))) int oref_dg_replay(const oref_
       }
       core.end_token({}, c->rows ? c->rows : 1);
       if (c->reset_at && tok + 1 == c->reset_at) core.reset_open();
+      if (c->round_every && (tok + 1) % c->round_every == 0) {  // ss_dg_round between tokens, nothing kept
+        ts::DgRoundIn in;
+        in.budget_bytes = c->round_budget;
+        in.max_units = c->round_max_units;
+        in.hysteresis = double(c->round_hysteresis);
+        in.decay = double(c->round_decay);
+        const ts::DgRoundOut r = core.round(in, {});
+        rsum[0] += 1;
+        rsum[1] += r.promoted_to_device;
+        rsum[2] += r.promoted_to_pinned;
+        rsum[3] += r.demoted_from_device;
+        rsum[4] += r.dropped_to_file;
+        rsum[5] += r.bytes_read + r.bytes_h2d + r.bytes_written_back;
+      }
+      if (c->rstats) std::memcpy(c->rstats + size_t(tok) * 6, rsum, sizeof rsum);
       std::memcpy(tables + size_t(tok) * keys, t.table_.data(), size_t(keys) * 4);
       const ts::DgStats& s = core.stats();
       const uint64_t v[OREF_NSTATS] = {s.tokens,          s.lookups,     s.misses,        s.covered,

@@ -11,7 +11,8 @@ import tempfile
 HERE = os.path.dirname(os.path.abspath(__file__))
 STRUCTS = ["ss_budget", "ss_options", "ss_plan_totals", "ss_layer_stats", "ss_group", "ss_layer_view",
            "ss_exclusive_stats", "ss_snapshot_info", "ss_dg_part", "ss_dg_device_view", "ss_dg_unit",
-           "ss_dg_layer_timeline", "ss_dg_boundary_timeline", "ss_dg_stats", "ss_file_identity"]
+           "ss_dg_layer_timeline", "ss_dg_boundary_timeline", "ss_dg_stats", "ss_file_identity",
+           "ss_dg_round_params", "ss_dg_round_result"]
 
 
 def fields_of(header, struct):

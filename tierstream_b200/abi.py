@@ -141,7 +141,9 @@ class dg_replay_config(C.Structure):
                 ("home_blocks", u32), ("disk_staging", u32), ("disk", C.POINTER(C.c_uint8)),
                 ("xstats", C.POINTER(u64)), ("reset_at", u32), ("reserved", u32), ("policy", u32), ("rows", u32),
                 ("w_trans", u32), ("w_freq", u32), ("w_rec", u32), ("reserved2", u32),
-                ("profile", C.POINTER(u32))]
+                ("profile", C.POINTER(u32)), ("round_every", u32), ("round_max_units", u32),
+                ("round_hysteresis", C.c_float), ("round_decay", C.c_float), ("round_budget", u64),
+                ("rstats", C.POINTER(u64))]
 
 
 class tsb_peer_tier(C.Structure):

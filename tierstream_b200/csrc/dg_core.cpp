@@ -2,6 +2,7 @@
 
 #include <algorithm>
 #include <chrono>
+#include <cmath>
 
 #include "errors.hpp"
 
@@ -28,6 +29,8 @@ SlotCache::SlotCache(const CacheConfig& cfg, Mover* m) : c_(cfg), m_(m) {
   require(uint64_t(c_.blocks) + c_.disk_staging < 0x7fffffffull, SS_E_INVALID, "device-gated: too many host blocks");
   stage_ev_.assign(c_.disk_staging, nullptr);
   run_.assign(c_.n_units.size(), 1);
+  rs_.assign(keys_, 0.0);
+  rhits_.assign(keys_, 0);
   if (c_.scored) {  // every score table allocated now (the service thread never allocates)
     require(c_.w_trans <= 1000 && c_.w_freq <= 1000 && c_.w_rec <= 1000 && c_.w_trans + c_.w_freq + c_.w_rec == 1000,
             SS_E_INVALID, "device-gated: score weights must each be 0..1000 and sum to 1000");
@@ -643,6 +646,10 @@ void SlotCache::serve_use(uint32_t g, const uint32_t* ids, uint32_t n, uint64_t 
   std::sort(uniq_.begin(), uniq_.end());
   uniq_.erase(std::unique(uniq_.begin(), uniq_.end()), uniq_.end());
   if (c_.scored) score_history(g);  // (the union saved before a prediction reuses uniq_)
+  for (uint32_t id : uniq_) {  // placement rounds: the tokens that routed the unit since the last round
+    uint32_t& h = rhits_[key(g, id)];
+    if (h != UINT32_MAX) ++h;
+  }
   for (uint32_t id : uniq_) {
     bool miss = false;
     for (uint32_t i = 0; i < n; ++i)
@@ -969,6 +976,283 @@ void SlotCache::load_counts(const std::vector<std::vector<uint32_t>>& cells) {
   }
 }
 
+// ---- placement rounds ----
+// Decay and add the hits; order the movable units (device homes coldest first, pinned and file homes hottest first;
+// ties: recency position, then key); then (a) pinned -> device: into a free slot while the device holds less than its
+// share (persistent slots - spare target - kept - coming), else in place of the coldest device unit when hotter by the
+// hysteresis factor (the demoted unit back to its clean block, or written back into a free block, or with the file
+// tier into the block of the coldest pinned unit, dropped to its file); (b) file tier: a file unit read into the block
+// of the coldest pinned unit (dropped to its file) when hotter by the hysteresis factor. A unit with no count never
+// moves; every step checks the budgets and the cancellation first (dg_core.cpp:2592-2897).
+RoundOut SlotCache::round(const RoundIn& in, const std::vector<uint32_t>& kept_keys) {
+  const auto t0 = std::chrono::steady_clock::now();
+  round_state_.store(kRoundRunning, std::memory_order_release);
+  struct Idle {
+    std::atomic<int>& s;
+    ~Idle() { s.store(kRoundIdle, std::memory_order_release); }
+  } idle{round_state_};
+  require(std::isfinite(in.decay) && in.decay >= 0 && in.decay <= 1, SS_E_INVALID, "ss_dg_round: decay must be 0..1");
+  require(std::isfinite(in.hysteresis) && in.hysteresis >= 1 && in.hysteresis <= 1e6, SS_E_INVALID,
+          "ss_dg_round: hysteresis must be 1..1e6");
+  require(in.flags == 0, SS_E_INVALID, "ss_dg_round: unknown flags");
+  std::vector<uint8_t> kept(keys_, 0);
+  size_t n_kept = 0;
+  for (uint32_t k : kept_keys)
+    if (k < keys_ && !kept[k]) {
+      kept[k] = 1;
+      ++n_kept;
+    }
+  for (uint32_t k = 0; k < keys_; ++k)
+    if (e_[k].home == Home::Bank) broken("a bank unit between tokens");
+  stamp_room("ss_dg_round");
+  drain();  // everything settled: copies, deferred and recorded write-backs collected
+  for (const Writeback& w : wbs_) m_->event_sync(w.done);
+  collect();
+  if (!wbs_.empty()) broken("ss_dg_round: write-backs not collected");
+  for (uint32_t k = 0; k < keys_; ++k) {
+    rs_[k] = in.decay * rs_[k] + double(rhits_[k]);
+    rhits_[k] = 0;
+  }
+
+  RoundOut r;
+  const uint64_t ub = unit_bytes_;
+  uint64_t spent = 0;
+  uint32_t moved = 0;
+  auto fits = [&](uint64_t b) { return !in.budget_bytes || (spent <= in.budget_bytes && b <= in.budget_bytes - spent); };
+  auto cancelled = [&] {
+    if (round_state_.load(std::memory_order_acquire) == kRoundCancel) r.cancelled = 1;
+    return r.cancelled != 0;
+  };
+  std::vector<uint32_t> pos(keys_, 0), hpos(keys_, 0);  // recency positions, least recent first
+  {
+    uint32_t i = 0;
+    for (uint32_t k = tail_; k != kNil; k = e_[k].prev) pos[k] = i++;
+  }
+  auto hotter = [&](uint32_t a, uint32_t b) { return rs_[a] != rs_[b] ? rs_[a] > rs_[b] : a < b; };
+  auto colder_dev = [&](uint32_t a, uint32_t b) {
+    if (rs_[a] != rs_[b]) return rs_[a] < rs_[b];
+    return pos[a] != pos[b] ? pos[a] < pos[b] : a < b;
+  };
+  auto colder_host = [&](uint32_t a, uint32_t b) {
+    if (rs_[a] != rs_[b]) return rs_[a] < rs_[b];
+    return hpos[a] != hpos[b] ? hpos[a] < hpos[b] : a < b;
+  };
+  std::vector<uint32_t> dev, host, file;
+  size_t n_coming = 0;
+  for (uint32_t k = 0; k < keys_; ++k) {
+    const Entry& x = e_[k];
+    if (x.home == Home::Coming) ++n_coming;
+    if (kept[k] || x.wb_pending) continue;
+    if (x.home == Home::Device) dev.push_back(k);
+    else if (x.home == Home::Host) host.push_back(k);
+    else if (x.home == Home::File) file.push_back(k);
+  }
+  std::sort(dev.begin(), dev.end(), colder_dev);
+  std::sort(host.begin(), host.end(), hotter);
+  std::sort(file.begin(), file.end(), hotter);
+  int64_t room = int64_t(c_.persistent_slots) - int64_t(c_.spare_target) - int64_t(n_kept) - int64_t(n_coming) -
+                 int64_t(dev.size());
+  const Mover::Stream ws = c_.wb_on_d2h ? Mover::kD2h : Mover::kDem;
+  auto account = [&] {
+    r.ns = uint64_t(
+        std::chrono::duration_cast<std::chrono::nanoseconds>(std::chrono::steady_clock::now() - t0).count());
+    ++st_.round_count;
+    st_.round_units += uint64_t(r.promoted_to_device) + r.promoted_to_pinned + r.demoted_from_device + r.dropped_to_file;
+    st_.round_bytes += r.bytes_read + r.bytes_h2d + r.bytes_written_back;
+    st_.round_ns += r.ns;
+    st_.round_cancelled += r.cancelled;
+  };
+  // a pinned unit into `slot`: its home changes once the copy and its entry were accepted and the demand stream synced;
+  // a cancellation seen then drops it (the slot free again, the unit keeps its block)
+  auto promote = [&](uint32_t k, int32_t slot) {
+    Entry& x = e_[k];
+    const int32_t b = x.block;
+    try {
+      m_->h2d(Mover::kDem, slot, b, k);
+      publish(Mover::kDem, k, slot);
+      m_->sync(Mover::kDem);
+    } catch (...) {
+      table_[k] = -1;
+      free_slots_.push_back(slot);
+      throw;
+    }
+    spent += ub;
+    r.bytes_h2d += ub;
+    if (cancelled()) {
+      table_[k] = -1;
+      free_slots_.push_back(slot);
+      return false;
+    }
+    hunlink(k);
+    free_blocks_.push_back(b);
+    x.block = -1;
+    x.slot = slot;
+    x.home = Home::Device;
+    push_front(k);
+    ++on_device_;
+    ++r.promoted_to_device;
+    return true;
+  };
+  // a block for a demoted unit's write-back: a free one, else (file tier) the coldest pinned unit's, dropped to its
+  // file (never `except`); -1 when none
+  size_t hback = host.size();
+  auto wb_block = [&](uint32_t except) -> int32_t {
+    if (!free_blocks_.empty()) {
+      const int32_t b = free_blocks_.back();
+      free_blocks_.pop_back();
+      return b;
+    }
+    if (!c_.disk_tier) return -1;
+    while (hback > 0) {
+      const uint32_t p = host[--hback];
+      Entry& y = e_[p];
+      if (p == except || y.home != Home::Host) continue;
+      hunlink(p);
+      const int32_t b = y.block;
+      y.block = -1;
+      y.home = Home::File;
+      ++on_file_;
+      ++r.dropped_to_file;
+      return b;
+    }
+    return -1;
+  };
+  // (b)'s reads: one at a time (synchronous), each committed at the next read or at the end
+  struct Rd {
+    uint32_t key;
+    int32_t block;
+  };
+  std::deque<Rd> reads;
+  auto end_read = [&] {
+    const Rd rd = reads.front();
+    reads.pop_front();
+    r.bytes_read += ub;
+    if (cancelled()) {  // the block free again, the unit stays in its file
+      free_blocks_.push_back(rd.block);
+      return;
+    }
+    Entry& x = e_[rd.key];
+    --on_file_;
+    x.home = Home::Host;
+    x.block = rd.block;
+    hpush(rd.key);
+    ++r.promoted_to_pinned;
+  };
+  try {
+    size_t j = 0;
+    for (size_t i = 0; i < host.size() && moved < in.max_units; ++i) {  // (a) pinned -> device
+      const uint32_t c = host[i];
+      if (!(rs_[c] > 0)) break;
+      if (e_[c].home != Home::Host) continue;  // (dropped to its file for a write-back block)
+      if (cancelled()) break;
+      if (room > 0 && free_slots_.size() > c_.spare_target) {  // the device holds less than its share
+        if (!fits(ub)) break;
+        const int32_t slot = free_slots_.back();
+        free_slots_.pop_back();
+        if (!promote(c, slot)) break;
+        --room;
+        ++moved;
+        continue;
+      }
+      if (j >= dev.size()) break;
+      const uint32_t v = dev[j];
+      if (!(rs_[c] > in.hysteresis * rs_[v])) break;
+      Entry& y = e_[v];
+      if (!fits(ub + (y.backed ? 0 : ub))) break;
+      const int32_t slot = y.slot;
+      if (y.backed) {  // a clean copy: its block is its home again, no write
+        unlink(v);
+        --on_device_;
+        table_[v] = -1;
+        to_lower(v);
+      } else {
+        const int32_t b = wb_block(c);
+        if (b < 0) break;
+        try {
+          m_->d2h(ws, slot, b, -1, v);
+          m_->sync(ws);
+        } catch (...) {
+          free_blocks_.push_back(b);  // the unit keeps its slot (its only copy)
+          throw;
+        }
+        unlink(v);
+        --on_device_;
+        table_[v] = -1;
+        y.home = Home::Host;
+        y.slot = -1;
+        y.block = b;
+        hpush(v);
+        spent += ub;
+        r.bytes_written_back += ub;
+      }
+      ++j;
+      ++r.demoted_from_device;
+      if (!promote(c, slot)) break;  // (cancelled: the demoted unit's slot stays free)
+      ++moved;
+    }
+    if (c_.disk_tier && !r.cancelled) {  // (b) file -> pinned, in place of the coldest pinned units
+      std::vector<uint32_t> pinned;
+      for (uint32_t k = 0; k < keys_; ++k)
+        if (e_[k].home == Home::Host && !kept[k] && !e_[k].wb_pending) pinned.push_back(k);
+      uint32_t hi = 0;
+      for (uint32_t k = htail_; k != kNil; k = e_[k].hprev) hpos[k] = hi++;  // after (a)'s pushes
+      std::sort(pinned.begin(), pinned.end(), colder_host);
+      size_t pv = 0;
+      for (size_t i = 0; i < file.size() && moved < in.max_units && pv < pinned.size(); ++i) {
+        const uint32_t c = file[i];
+        if (!(rs_[c] > 0)) break;
+        if (e_[c].home != Home::File) continue;
+        if (cancelled()) break;
+        const uint32_t p = pinned[pv];
+        if (!(rs_[c] > in.hysteresis * rs_[p])) break;
+        if (!fits(ub)) break;
+        if (!reads.empty()) end_read();
+        if (r.cancelled) break;
+        ++pv;
+        Entry& y = e_[p];  // dropped to its file (no copy): its block is quiescent
+        hunlink(p);
+        const int32_t b = y.block;
+        y.block = -1;
+        y.home = Home::File;
+        ++on_file_;
+        ++r.dropped_to_file;
+        try {
+          m_->read_unit(c, b);
+        } catch (...) {
+          free_blocks_.push_back(b);
+          throw;
+        }
+        reads.push_back({c, b});
+        spent += ub;
+        ++moved;
+      }
+      while (!reads.empty()) end_read();
+    }
+    m_->upload_table(table_.data(), keys_);  // (syncs the demand stream) every changed entry
+  } catch (...) {
+    for (const Rd& rd : reads) free_blocks_.push_back(rd.block);  // never committed: their units stay in their files
+    reads.clear();
+    try {  // the moves made so far go up (a failed device fails this too; the caller then poisons the context)
+      m_->upload_table(table_.data(), keys_);
+    } catch (...) {
+    }
+    account();
+    throw;
+  }
+  account();
+  return r;
+}
+
+void SlotCache::seed_round_counts(const std::vector<uint32_t>& keys, const std::vector<float>& counts) {
+  require(keys.size() == counts.size(), SS_E_INVALID, "ss_dg_round_seed_counts: keys and counts differ in length");
+  for (size_t i = 0; i < keys.size(); ++i) {
+    require(keys[i] < keys_, SS_E_INVALID, "ss_dg_round_seed_counts: unit out of range");
+    require(std::isfinite(counts[i]) && counts[i] >= 0, SS_E_INVALID,
+            "ss_dg_round_seed_counts: counts must be finite and >= 0");
+  }
+  for (size_t i = 0; i < keys.size(); ++i) rs_[keys[i]] = double(counts[i]);
+}
+
 uint32_t SlotCache::seed(const std::vector<uint32_t>& keys) {
   stamp_room("ss_seed");
   if (!coming_.empty()) m_->sync(Mover::kPf);
@@ -1157,6 +1441,8 @@ void SlotCache::reset_open() {
   apply_wb_defer();
   std::copy(open_e_.begin(), open_e_.end(), e_.begin());
   reset_score();  // the history's open state (a profile's counts, or none)
+  std::fill(rs_.begin(), rs_.end(), 0.0);  // placement rounds: the counts start over
+  std::fill(rhits_.begin(), rhits_.end(), 0u);
   backed_ = 0;  // clean copies are dropped: the open holds none
   std::copy(open_table_.begin(), open_table_.end(), table_.begin());
   free_slots_ = open_free_slots_;

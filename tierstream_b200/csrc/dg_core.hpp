@@ -30,9 +30,14 @@
 //     transition count table between successive tokens' unions of routed ids, a frequency ring of the last 16 unions
 //     and each unit's last routed token; the boundary takes, among the same eligible units, the lowest integer scores
 //     w_t P + w_f F + w_r Rec first (ties: the older use, then the less recent unit) instead of the recency tail
-//     (dg_core.cpp:1933-2130, 1811-1826).
+//     (dg_core.cpp:1933-2130, 1811-1826);
+//   - placement rounds (between tokens): a decayed count per unit of the tokens that routed it; a round promotes the
+//     hottest pinned units to the device (into free slots while the device holds less than its share, else in place of
+//     the coldest device unit when hotter by the hysteresis factor) and, with the file tier, the hottest file units into
+//     the blocks of the coldest pinned ones (dg_core.cpp:2592-2897).
 #pragma once
 
+#include <atomic>
 #include <cstdint>
 #include <deque>
 #include <functional>
@@ -120,6 +125,22 @@ struct CacheStats {
   // taken by score, layers scored and the candidates they ranked, saturated transition increments, selection time
   uint64_t score_fallbacks = 0, scored_victims = 0, score_layers = 0, score_candidates = 0, score_saturated = 0;
   uint64_t score_ns = 0;
+  // placement rounds: rounds run, units whose home they changed, bytes moved, host time, rounds cancelled
+  uint64_t round_count = 0, round_units = 0, round_bytes = 0, round_ns = 0, round_cancelled = 0;
+};
+
+// A placement round's limits and what it did (ss_dg_round_params / ss_dg_round_result without the struct sizes).
+struct RoundIn {
+  uint64_t budget_bytes = 0;  // file reads + host-to-device copies + write-backs (0 = no limit)
+  uint32_t max_units = 96;    // promotions at most
+  double hysteresis = 1.25;   // a unit replaces another only when its count is above this x the other's
+  double decay = 0.85;        // s = decay x s + hits since the last round
+  uint32_t flags = 0;
+};
+struct RoundOut {
+  uint32_t promoted_to_device = 0, promoted_to_pinned = 0, demoted_from_device = 0, dropped_to_file = 0;
+  uint32_t cancelled = 0;
+  uint64_t bytes_read = 0, bytes_h2d = 0, bytes_written_back = 0, ns = 0;
 };
 
 struct LayerCounts {
@@ -193,6 +214,16 @@ class SlotCache {
   // A score profile's transition counts (units(g)^2 per gated layer, row-major [previous unit][unit]) as the open
   // state of the tables (scored only; kept for reset_open).
   void load_counts(const std::vector<std::vector<uint32_t>>& cells);
+  // Between tokens: one placement round (kept: keys that never move). Every copy landed and the table is uploaded when
+  // it returns.
+  RoundOut round(const RoundIn& in, const std::vector<uint32_t>& kept);
+  // Any thread: a running round stops at its next unit boundary (no effect when none runs).
+  void cancel_round() {
+    int running = kRoundRunning;
+    round_state_.compare_exchange_strong(running, kRoundCancel, std::memory_order_acq_rel);
+  }
+  void seed_round_counts(const std::vector<uint32_t>& keys, const std::vector<float>& counts);
+  double round_count(uint32_t k) const { return rs_[k]; }
   uint32_t seed(const std::vector<uint32_t>& keys);
   void drain();
   // Restores the open placement, moving only misplaced units; `plan` receives the slot-to-slot moves in execution
@@ -297,6 +328,10 @@ class SlotCache {
   std::vector<uint8_t> run_;
   uint64_t epoch_ = 0, stamp_ = 0, open_stamp_ = 0;
   std::vector<ScoreCand> select_heap_;
+  std::vector<double> rs_;         // placement rounds: the decayed counts
+  std::vector<uint32_t> rhits_;    // the tokens that routed each unit since the last round
+  static constexpr int kRoundIdle = 0, kRoundRunning = 1, kRoundCancel = 2;
+  std::atomic<int> round_state_{kRoundIdle};
   std::deque<Writeback> wbs_;
   std::deque<Deferred> deferred_;
   Mover::Stream wb_stream_ = Mover::kDem;

@@ -138,6 +138,7 @@ void dg_replay(const tsb_dg_replay_config* c, const int32_t* ids, const int32_t*
       std::memcpy(dst, src_units + size_t(k) * m.unit_, m.unit_);
     }
   std::vector<uint32_t> row(c->n_ids), pred(c->n_pred);
+  uint64_t rsum[6] = {0, 0, 0, 0, 0, 0};
   for (uint32_t t = 0; t < c->tokens; ++t) {
     core.begin_token(t + 1);
     for (uint32_t g = 0; g < c->n_gated; ++g) {
@@ -164,6 +165,21 @@ void dg_replay(const tsb_dg_replay_config* c, const int32_t* ids, const int32_t*
     }
     core.end_token({}, c->rows ? c->rows : 1);
     if (c->reset_at && t + 1 == c->reset_at) core.reset_open();
+    if (c->round_every && (t + 1) % c->round_every == 0) {
+      RoundIn in;
+      in.budget_bytes = c->round_budget;
+      in.max_units = c->round_max_units;
+      in.hysteresis = double(c->round_hysteresis);
+      in.decay = double(c->round_decay);
+      const RoundOut r = core.round(in, {});
+      rsum[0] += 1;
+      rsum[1] += r.promoted_to_device;
+      rsum[2] += r.promoted_to_pinned;
+      rsum[3] += r.demoted_from_device;
+      rsum[4] += r.dropped_to_file;
+      rsum[5] += r.bytes_read + r.bytes_h2d + r.bytes_written_back;
+    }
+    if (c->rstats) std::memcpy(c->rstats + size_t(t) * 6, rsum, sizeof rsum);
     std::memcpy(tables + size_t(t) * keys, m.table_.data(), size_t(keys) * 4);
     const CacheStats& s = core.stats();
     const uint64_t v[16] = {s.tokens,        s.lookups,     s.misses,          s.covered,     s.fetched,

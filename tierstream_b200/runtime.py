@@ -245,7 +245,8 @@ class TokenGraph:
 def replay_config(n_units, part_bytes, persistent_slots, bank_slots, blocks, spare_target, order, tokens, n_ids,
                   n_pred=0, prefetch_reserve=0xFFFFFFFF, prefetch_per_layer=4, prefetch_per_token=48, wb_defer=1,
                   wb_on_d2h=1, wb_layer_bytes=0, wb_max_outstanding=0, move_bytes=0, inclusive=0, disk=None,
-                  home_blocks=0, disk_staging=0, disk_prefetch=0, policy=0, rows=1, weights=None, profile=None):
+                  home_blocks=0, disk_staging=0, disk_prefetch=0, policy=0, rows=1, weights=None, profile=None,
+                  round_every=0, round_max_units=96, round_hysteresis=1.25, round_decay=0.85, round_budget=0):
     """A dg_replay_config with its arrays kept alive on the returned object. disk (file tier): one flag per key for
     the plan's disk units (blocks then counts home_blocks + the spare blocks); xstats is attached by replay().
     policy (scored eviction): 0 LRU, 1 SCORED, 2 SCORED_AUTO, with each boundary's row count `rows`, weights
@@ -268,6 +269,8 @@ def replay_config(n_units, part_bytes, persistent_slots, bank_slots, blocks, spa
     c.order = keep["order"]
     c.tokens, c.n_ids, c.n_pred, c.move_bytes, c.inclusive = tokens, n_ids, n_pred, move_bytes, inclusive
     c.policy, c.rows = policy, rows
+    c.round_every, c.round_max_units, c.round_hysteresis, c.round_decay, c.round_budget = \
+        round_every, round_max_units, round_hysteresis, round_decay, round_budget
     if weights:
         c.w_trans, c.w_freq, c.w_rec = weights
     if profile is not None:
@@ -282,11 +285,12 @@ def replay_config(n_units, part_bytes, persistent_slots, bank_slots, blocks, spa
     return c
 
 
-def replay(cfg, ids, preds=None, src_units=None, want_reads=False, xstats=None):
+def replay(cfg, ids, preds=None, src_units=None, want_reads=False, xstats=None, rstats=None):
     """This library's deterministic replay (tsb_test_dg_replay): (tables, stats[, read_sum]). xstats: an optional
     uint64 array [tokens][6] filled with the file tier's counters after each boundary."""
     keys = sum(cfg.n_units[i] for i in range(cfg.n_gated))
     cfg.xstats = xstats.ctypes.data_as(C.POINTER(C.c_uint64)) if xstats is not None else None
+    cfg.rstats = rstats.ctypes.data_as(C.POINTER(C.c_uint64)) if rstats is not None else None  # [tokens][6] rounds
     ids = np.ascontiguousarray(ids, dtype=np.int32)
     tables = np.empty((cfg.tokens, keys), dtype=np.int32)
     stats = np.empty((cfg.tokens, 16), dtype=np.uint64)
