@@ -74,3 +74,15 @@ def test_struct_layouts_match_reference_header():
         assert got[struct]["__sizeof__"] == g["size"], struct
         for f, off in g["fields"].items():
             assert got[struct][f] == off, "%s.%s" % (struct, f)
+
+
+def test_round_defaults_and_cancel_without_a_context():
+    """ss_dg_round_defaults fills the reference's defaults; ss_dg_round_cancel refuses a missing context."""
+    import ctypes as C
+    from tierstream_b200 import abi
+    lib = abi.load()
+    p = abi.ss_dg_round_params()
+    lib.ss_dg_round_defaults_sized(C.byref(p), C.sizeof(p))
+    assert (p.struct_size, p.flags, p.budget_bytes, p.max_units) == (C.sizeof(p), 0, 0, 96)
+    assert abs(p.hysteresis - 1.25) < 1e-7 and abs(p.decay - 0.85) < 1e-7
+    assert lib.ss_dg_round_cancel(None) == abi.SS_E_INVALID

@@ -1,7 +1,8 @@
-"""Scored eviction (SS_POLICY_SCORED) through the device-gated context on the GPU: under the deterministic schedule the
-device's slot table after every token equals the reference DgCore's replay with the same policy (with and without a
-TSSCPRF1 profile of transition counts), every routed unit's bytes are the source's, and ss_dg_set_policy switches
-between LRU and SCORED between tokens (refused for a context opened with LRU, whose score tables do not exist)."""
+"""Scored eviction (SS_POLICY_SCORED) and placement rounds (ss_dg_round) through the device-gated context on the GPU:
+under the deterministic schedule the device's slot table after every token equals the reference DgCore's replay with
+the same policy (with and without a TSSCPRF1 profile of transition counts) or the same rounds, every routed unit's
+bytes are the source's, ss_dg_set_policy switches between LRU and SCORED between tokens (refused for a context opened
+with LRU, whose score tables do not exist), and the rounds' results sum to the reference's."""
 import os
 
 import numpy as np
@@ -76,5 +77,41 @@ def test_set_policy_needs_scoring_at_open(model):
     try:
         st = abi.load().ss_dg_set_policy(run.ctx.h, abi.SS_POLICY_SCORED)
         assert st == abi.SS_E_INVALID and b"set up at ss_open" in abi.load().ss_last_error()
+    finally:
+        run.close()
+
+
+@pytest.mark.parametrize("wb_defer", [0, 1])
+def test_rounds_match_reference(model, orc, ref, monkeypatch, wb_defer):
+    monkeypatch.setenv("TSB_DG_DETERMINISTIC", "1")
+    m = model
+    G, U = m.layers, m.units
+    ids = synth.zipf_trace(30, G, U, 2, s=1.2, seed=51)
+    run = harness.DgRun(m, residents_per_layer=3, max_ids=2, wb_defer=wb_defer)
+    try:
+        res = run.resident_keys
+        P = G * U - len(res)
+        cfg = runtime.replay_config([U] * G, list(m.part_bytes), persistent_slots=len(res) + G, bank_slots=2,
+                                    blocks=P + G, spare_target=G, order=res, tokens=ids.shape[0], n_ids=2,
+                                    wb_defer=wb_defer, round_every=5)
+        r_ref = np.zeros((ids.shape[0], 6), dtype=np.uint64)
+        t_ref, s_ref = oracle.ref_replay(cfg, ids, rstats=r_ref)
+        want = expected_sums(m, orc)
+        sums = np.zeros(6, dtype=np.uint64)
+        for t in range(ids.shape[0]):
+            got = run.step(ids[t])
+            assert np.array_equal(got, want[np.arange(G)[:, None] * U + ids[t]]), "token %d read wrong bytes" % t
+            if (t + 1) % 5 == 0:
+                r = run.ctx.round()
+                sums += np.array([1, r["promoted_to_device"], r["promoted_to_pinned"], r["demoted_from_device"],
+                                  r["dropped_to_file"], r["bytes_read"] + r["bytes_h2d"] + r["bytes_written_back"]],
+                                 dtype=np.uint64)
+            assert np.array_equal(run.ctx.table(run.keys), t_ref[t]), "slot table differs after token %d" % t
+        assert np.array_equal(sums, r_ref[-1]) and sums[1] > 0
+        assert run.ctx.stats()["round_count"] == 6
+        run.ctx.check()
+        for L in range(G):
+            for u in range(U):
+                run.ctx.check_unit(L, u)
     finally:
         run.close()

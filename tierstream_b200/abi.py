@@ -122,7 +122,9 @@ _DG_STATS_U64_1 = ["tokens", "lookups", "misses", "covered", "fetched", "prefetc
                    "score_candidates", "score_saturated", "score_ns", "score_deferred", "score_last_ns",
                    "disk_reads", "disk_read_bytes", "disk_read_ns", "disk_stage_waits", "disk_drops", "disk_discards",
                    "inclusive_kept", "inclusive_drops", "disk_units", "backed_units", "disk_wait_ns",
-                   "disk_overlapped", "disk_max_in_flight", "disk_carried", "disk_carried_bytes"]
+                   "disk_overlapped", "disk_max_in_flight", "disk_carried", "disk_carried_bytes",
+                   "resident_units", "resident_evicted", "resident_bytes", "resident_ns", "round_count",
+                   "round_units", "round_bytes", "round_ns", "round_cancelled"]
 
 
 class ss_dg_stats(C.Structure):
@@ -144,6 +146,17 @@ class dg_replay_config(C.Structure):
                 ("profile", C.POINTER(u32)), ("round_every", u32), ("round_max_units", u32),
                 ("round_hysteresis", C.c_float), ("round_decay", C.c_float), ("round_budget", u64),
                 ("rstats", C.POINTER(u64))]
+
+
+class ss_dg_round_params(C.Structure):
+    _fields_ = [("struct_size", u32), ("flags", u32), ("budget_bytes", u64), ("max_units", u32),
+                ("hysteresis", C.c_float), ("decay", C.c_float), ("reserved0", u32)]
+
+
+class ss_dg_round_result(C.Structure):
+    _fields_ = [("struct_size", u32), ("promoted_to_device", u32), ("promoted_to_pinned", u32),
+                ("demoted_from_device", u32), ("dropped_to_file", u32), ("cancelled", u32), ("bytes_read", u64),
+                ("bytes_h2d", u64), ("bytes_written_back", u64), ("ns", u64)]
 
 
 class tsb_peer_tier(C.Structure):
@@ -214,6 +227,10 @@ _PROTOS = {
     "ss_dg_boundary_timeline_sized": (C.c_int, [vp, P(ss_dg_boundary_timeline), u32]),
     "ss_dg_reset_open": (C.c_int, [vp]),
     "ss_dg_set_policy": (C.c_int, [vp, C.c_int]),
+    "ss_dg_round_defaults_sized": (None, [P(ss_dg_round_params), u32]),
+    "ss_dg_round_sized": (C.c_int, [vp, P(ss_dg_round_params), P(ss_dg_round_result), u32]),
+    "ss_dg_round_cancel": (C.c_int, [vp]),
+    "ss_dg_round_seed_counts": (C.c_int, [vp, vp, P(C.c_float), u32]),
     "ss_test_dg_check": (C.c_int, [vp]),
     "ss_test_dg_flags": (C.c_int, [vp, u32]),
     "ss_test_dg_pressure": (C.c_int, [vp, u32, u32]),

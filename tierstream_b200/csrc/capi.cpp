@@ -858,13 +858,65 @@ ss_status ss_budget_in_dg_library(ss_budget_in*, const ss_desc*, const ss_option
   return unsupported("ss_budget_in_dg_library");
 }
 ss_status ss_dg_make_resident(ss_ctx*, int, const int32_t*, int) { return unsupported("ss_dg_make_resident"); }
-void ss_dg_round_defaults_sized(ss_dg_round_params*, uint32_t) {}
-ss_status ss_dg_round_sized(ss_ctx*, const ss_dg_round_params*, ss_dg_round_result*, uint32_t) {
-  return unsupported("ss_dg_round");
+namespace {
+void round_defaults(ss_dg_round_params* p) {
+  *p = ss_dg_round_params{};
+  p->struct_size = uint32_t(sizeof *p);
+  p->budget_bytes = 0;
+  p->max_units = 96;
+  p->hysteresis = 1.25f;
+  p->decay = 0.85f;
 }
-ss_status ss_dg_round_cancel(ss_ctx*) { return unsupported("ss_dg_round_cancel"); }
-ss_status ss_dg_round_seed_counts(ss_ctx*, const ss_dg_unit*, const float*, uint32_t) {
-  return unsupported("ss_dg_round_seed_counts");
+}  // namespace
+void ss_dg_round_defaults_sized(ss_dg_round_params* p, uint32_t size) { sized_defaults(p, size, round_defaults); }
+ss_status ss_dg_round_sized(ss_ctx* c, const ss_dg_round_params* p, ss_dg_round_result* out, uint32_t size) {
+  return ctx_guard(c, [&] {
+    need(!out || size >= sizeof(uint32_t), "ss_dg_round: bad result size");
+    const ss_dg_round_params v = versioned(p, round_defaults, "ss_dg_round");
+    tsb::RoundIn in;
+    in.flags = v.flags;
+    in.budget_bytes = v.budget_bytes;
+    in.max_units = v.max_units;
+    in.hysteresis = double(v.hysteresis);
+    in.decay = double(v.decay);
+    tsb::DgContext& dg = dg_of(c, "ss_dg_round");
+    auto fill = [&] {  // on success, and on a failure after the round began
+      if (!out) return;
+      const tsb::RoundOut& r = dg.last_round();
+      ss_dg_round_result x{};
+      x.promoted_to_device = r.promoted_to_device;
+      x.promoted_to_pinned = r.promoted_to_pinned;
+      x.demoted_from_device = r.demoted_from_device;
+      x.dropped_to_file = r.dropped_to_file;
+      x.cancelled = r.cancelled;
+      x.bytes_read = r.bytes_read;
+      x.bytes_h2d = r.bytes_h2d;
+      x.bytes_written_back = r.bytes_written_back;
+      x.ns = r.ns;
+      give_sized(out, size, x);
+    };
+    try {
+      dg.round(in);
+    } catch (...) {
+      fill();
+      throw;
+    }
+    fill();
+  });
+}
+ss_status ss_dg_round_cancel(ss_ctx* c) {
+  if (!c || !c->dg) {
+    g_err = "ss_dg_round_cancel: not a device-gated context";
+    return SS_E_INVALID;
+  }
+  c->dg->round_cancel();
+  return SS_OK;
+}
+ss_status ss_dg_round_seed_counts(ss_ctx* c, const ss_dg_unit* units, const float* counts, uint32_t n) {
+  return ctx_guard(c, [&] {
+    need(n == 0 || (units && counts), "ss_dg_round_seed_counts: bad arguments");
+    dg_of(c, "ss_dg_round_seed_counts").round_seed_counts(units, counts, n);
+  });
 }
 void ss_devprof_detect_opts_defaults_sized(ss_devprof_detect_opts*, uint32_t) {}
 ss_status ss_devprof_detect(const ss_devprof_detect_opts*, ss_devprof**) { return unsupported("ss_devprof_detect"); }

@@ -9,6 +9,7 @@
 
 #include "desc.hpp"
 #include "plan.hpp"
+#include "dg_core.hpp"
 #include "strix_stream/ss.h"
 
 namespace tsb {
@@ -42,6 +43,12 @@ class DgContext {
   virtual void end(uint32_t rows) = 0;
   // Between tokens: LRU, SCORED or SCORED_AUTO (scoring must have been set up at the open)
   virtual void set_policy(uint32_t policy) = 0;
+  // Placement rounds: one round between tokens (its result kept for last_round, also after a failure once it began);
+  // a cancellation from any thread; counts set from a shipped profile
+  virtual void round(const RoundIn& in) = 0;
+  virtual const RoundOut& last_round() const = 0;
+  virtual void round_cancel() = 0;
+  virtual void round_seed_counts(const ss_dg_unit* units, const float* counts, uint32_t n) = 0;
   virtual void seed(int layer, const int32_t* units, int n) = 0;
   virtual void check_unit(int layer, int unit) = 0;
   virtual void device_view(ss_dg_device_view* v) const = 0;

@@ -991,6 +991,7 @@ RoundOut SlotCache::round(const RoundIn& in, const std::vector<uint32_t>& kept_k
     std::atomic<int>& s;
     ~Idle() { s.store(kRoundIdle, std::memory_order_release); }
   } idle{round_state_};
+  last_round_ = RoundOut{};
   require(std::isfinite(in.decay) && in.decay >= 0 && in.decay <= 1, SS_E_INVALID, "ss_dg_round: decay must be 0..1");
   require(std::isfinite(in.hysteresis) && in.hysteresis >= 1 && in.hysteresis <= 1e6, SS_E_INVALID,
           "ss_dg_round: hysteresis must be 1..1e6");
@@ -1061,6 +1062,7 @@ RoundOut SlotCache::round(const RoundIn& in, const std::vector<uint32_t>& kept_k
     st_.round_bytes += r.bytes_read + r.bytes_h2d + r.bytes_written_back;
     st_.round_ns += r.ns;
     st_.round_cancelled += r.cancelled;
+    last_round_ = r;
   };
   // a pinned unit into `slot`: its home changes once the copy and its entry were accepted and the demand stream synced;
   // a cancellation seen then drops it (the slot free again, the unit keeps its block)

@@ -223,6 +223,8 @@ class SlotCache {
     round_state_.compare_exchange_strong(running, kRoundCancel, std::memory_order_acq_rel);
   }
   void seed_round_counts(const std::vector<uint32_t>& keys, const std::vector<float>& counts);
+  // The last round's result (also after a failure once it began; zeros before the first).
+  const RoundOut& last_round() const { return last_round_; }
   double round_count(uint32_t k) const { return rs_[k]; }
   uint32_t seed(const std::vector<uint32_t>& keys);
   void drain();
@@ -332,6 +334,7 @@ class SlotCache {
   std::vector<uint32_t> rhits_;    // the tokens that routed each unit since the last round
   static constexpr int kRoundIdle = 0, kRoundRunning = 1, kRoundCancel = 2;
   std::atomic<int> round_state_{kRoundIdle};
+  RoundOut last_round_;
   std::deque<Writeback> wbs_;
   std::deque<Deferred> deferred_;
   Mover::Stream wb_stream_ = Mover::kDem;

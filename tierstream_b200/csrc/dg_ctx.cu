@@ -1135,6 +1135,11 @@ class CudaDgContext final : public DgContext {
     s.score_candidates = d(c.score_candidates, base_.score_candidates);
     s.score_saturated = d(c.score_saturated, base_.score_saturated);
     s.score_ns = d(c.score_ns, base_.score_ns);
+    s.round_count = d(c.round_count, base_.round_count);
+    s.round_units = d(c.round_units, base_.round_units);
+    s.round_bytes = d(c.round_bytes, base_.round_bytes);
+    s.round_ns = d(c.round_ns, base_.round_ns);
+    s.round_cancelled = d(c.round_cancelled, base_.round_cancelled);
     s.disk_queue_resolved = x_.disk_tier ? 1u : 0u;
     std::memcpy(out, &s, sizeof s);
   }
@@ -1226,6 +1231,27 @@ class CudaDgContext final : public DgContext {
     base_ = core_->stats();
     lbase_ = core_->layer_counts();
     timeline_valid_ = false;
+  }
+
+  void round(const RoundIn& in) override {
+    require(!in_token_, SS_E_INVALID, "ss_dg_round: between tokens only");
+    core_->round(in, keep_all());  // (a device failure poisons the context through the ABI's guard)
+  }
+  const RoundOut& last_round() const override { return core_->last_round(); }
+  void round_cancel() override { core_->cancel_round(); }
+  void round_seed_counts(const ss_dg_unit* units, const float* counts, uint32_t n) override {
+    require(!in_token_, SS_E_INVALID, "ss_dg_round_seed_counts: between tokens only");
+    std::vector<uint32_t> keys;
+    std::vector<float> v;
+    for (uint32_t i = 0; i < n; ++i) {
+      const int g = units[i].gated;
+      require(g >= 0 && uint32_t(g) < core_->gated() && units[i].unit >= 0 &&
+                  uint32_t(units[i].unit) < core_->units(uint32_t(g)),
+              SS_E_INVALID, "ss_dg_round_seed_counts: unit " + std::to_string(i) + " is out of range");
+      keys.push_back(core_->key(uint32_t(g), uint32_t(units[i].unit)));
+      v.push_back(counts[i]);
+    }
+    core_->seed_round_counts(keys, v);
   }
 
   void set_policy(uint32_t policy) override {

@@ -131,6 +131,17 @@ class DgContext:
     def reset_open(self):
         abi.check(abi.load().ss_dg_reset_open(self.h))
 
+    def round(self, **params):
+        """One placement round between tokens (ss_dg_round): params override the defaults (budget_bytes, max_units,
+        hysteresis, decay); returns the result's fields."""
+        p = abi.ss_dg_round_params()
+        abi.load().ss_dg_round_defaults_sized(C.byref(p), C.sizeof(p))
+        for k, v in params.items():
+            setattr(p, k, v)
+        r = abi.ss_dg_round_result()
+        abi.check(abi.load().ss_dg_round_sized(self.h, C.byref(p), C.byref(r), C.sizeof(r)))
+        return {n: getattr(r, n) for n, _ in r._fields_ if n != "struct_size"}
+
     def set_policy(self, policy):
         """Between tokens: SS_POLICY_LRU / SCORED / SCORED_AUTO (ss_dg_set_policy)."""
         abi.check(abi.load().ss_dg_set_policy(self.h, policy))
