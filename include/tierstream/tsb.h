@@ -98,6 +98,10 @@ typedef struct tsb_dg_replay_config {
   float round_hysteresis, round_decay;
   uint64_t round_budget;
   uint64_t* rstats;
+  /* the opt-in policies dg_no_admit, dg_clean_evict, dg_pf_revert_unused, dg_pf_strict_admit (0 / 1); pstats
+   * (optional): [tokens][5] clean_drops, clean_drop_bytes, pf_reverted, pf_revert_bytes, pf_strict_refused */
+  uint32_t no_admit, clean_evict, pf_revert, pf_strict;
+  uint64_t* pstats;
 } tsb_dg_replay_config;
 SS_API ss_status tsb_test_dg_replay(const tsb_dg_replay_config* cfg, const int32_t* ids, const int32_t* preds,
                                     int32_t* tables, uint64_t* stats, const uint8_t* src_units, uint64_t* read_sum);

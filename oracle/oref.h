@@ -43,6 +43,10 @@ typedef struct oref_dg_config {
   float round_hysteresis, round_decay;
   uint64_t round_budget;
   uint64_t* rstats;
+  /* opt-in policies (0 / 1); pstats (optional): [tokens][5] clean_drops, clean_drop_bytes, pf_reverted,
+   * pf_revert_bytes, pf_strict_refused */
+  uint32_t no_admit, clean_evict, pf_revert, pf_strict;
+  uint64_t* pstats;
 } oref_dg_config;
 #define OREF_NXSTATS 6
 

@@ -145,6 +145,10 @@ extern "C" __attribute__((visibility("default"))) int oref_dg_replay(const oref_
     cfg.scored = c->policy != 0;  // the bounded boundary selection, as its device-gated context configures it
     cfg.scored_auto = c->policy == 2;
     cfg.boundary_score = true;
+    cfg.no_admit = c->no_admit != 0;
+    cfg.clean_evict = c->clean_evict != 0;
+    cfg.pf_revert = c->pf_revert != 0;
+    cfg.pf_strict = c->pf_strict != 0;
     if (c->w_trans || c->w_freq || c->w_rec) {
       cfg.w_trans = c->w_trans;
       cfg.w_freq = c->w_freq;
@@ -222,6 +226,12 @@ extern "C" __attribute__((visibility("default"))) int oref_dg_replay(const oref_
         rsum[5] += r.bytes_read + r.bytes_h2d + r.bytes_written_back;
       }
       if (c->rstats) std::memcpy(c->rstats + size_t(tok) * 6, rsum, sizeof rsum);
+      if (c->pstats) {
+        const ts::DgStats& q = core.stats();
+        const uint64_t pv[5] = {q.clean_drops, q.clean_drop_bytes, q.pf_reverted, q.pf_revert_bytes,
+                                q.pf_strict_refused};
+        std::memcpy(c->pstats + size_t(tok) * 5, pv, sizeof pv);
+      }
       std::memcpy(tables + size_t(tok) * keys, t.table_.data(), size_t(keys) * 4);
       const ts::DgStats& s = core.stats();
       const uint64_t v[OREF_NSTATS] = {s.tokens,          s.lookups,     s.misses,        s.covered,

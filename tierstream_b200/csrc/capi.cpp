@@ -970,13 +970,17 @@ ss_status ss_pack_writer_record_end(ss_pack_writer*) { return unsupported("ss_pa
 ss_status ss_pack_writer_add(ss_pack_writer*, const ss_pack_record_spec*, const void*) { return unsupported("ss_pack_writer_add"); }
 ss_status ss_pack_writer_finish(ss_pack_writer*, char*) { return unsupported("ss_pack_writer_finish"); }
 void ss_pack_writer_abort(ss_pack_writer*) {}
-ss_status ss_dg_set_clean_evict(ss_ctx*, uint32_t) { return unsupported("ss_dg_set_clean_evict"); }
+ss_status ss_dg_set_clean_evict(ss_ctx* c, uint32_t on) {
+  return ctx_guard(c, [&] { dg_of(c, "ss_dg_set_clean_evict").set_clean_evict(on); });
+}
 ss_status ss_dg_begin_layer(ss_ctx*, int, int) { return unsupported("ss_dg_begin_layer"); }
 ss_status ss_dg_enqueue_export_part(ss_ctx*, int, int, const int32_t*, int, void*) {
   return unsupported("ss_dg_enqueue_export_part");
 }
 ss_status ss_dg_enqueue_wait_part(ss_ctx*, int, int, void*) { return unsupported("ss_dg_enqueue_wait_part"); }
 ss_status ss_dg_enqueue_end_layer(ss_ctx*, void*) { return unsupported("ss_dg_enqueue_end_layer"); }
-ss_status ss_dg_set_pf_revert_unused(ss_ctx*, uint32_t) { return unsupported("ss_dg_set_pf_revert_unused"); }
+ss_status ss_dg_set_pf_revert_unused(ss_ctx* c, uint32_t on) {
+  return ctx_guard(c, [&] { dg_of(c, "ss_dg_set_pf_revert_unused").set_pf_revert_unused(on); });
+}
 
 }  // extern "C"

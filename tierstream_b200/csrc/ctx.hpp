@@ -49,6 +49,9 @@ class DgContext {
   virtual const RoundOut& last_round() const = 0;
   virtual void round_cancel() = 0;
   virtual void round_seed_counts(const ss_dg_unit* units, const float* counts, uint32_t n) = 0;
+  // Between tokens: the opt-in policies dg_clean_evict and dg_pf_revert_unused switched at run time
+  virtual void set_clean_evict(uint32_t on) = 0;
+  virtual void set_pf_revert_unused(uint32_t on) = 0;
   virtual void seed(int layer, const int32_t* units, int n) = 0;
   virtual void check_unit(int layer, int unit) = 0;
   virtual void device_view(ss_dg_device_view* v) const = 0;

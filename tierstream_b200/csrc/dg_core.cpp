@@ -28,6 +28,9 @@ SlotCache::SlotCache(const CacheConfig& cfg, Mover* m) : c_(cfg), m_(m) {
           "device-gated: file tier options without the file tier");
   require(uint64_t(c_.blocks) + c_.disk_staging < 0x7fffffffull, SS_E_INVALID, "device-gated: too many host blocks");
   stage_ev_.assign(c_.disk_staging, nullptr);
+  require(!c_.no_admit || c_.bank_slots >= c_.max_ids, SS_E_CAPACITY,
+          "device-gated: dg_no_admit serves every miss through a bank slot: it needs " + std::to_string(c_.max_ids) +
+              " bank slots per bank (dg_max_ids), " + std::to_string(c_.bank_slots) + " configured");
   run_.assign(c_.n_units.size(), 1);
   rs_.assign(keys_, 0.0);
   rhits_.assign(keys_, 0);
@@ -204,6 +207,17 @@ void SlotCache::hunlink(uint32_t k) {
   x.in_hlist = false;
 }
 
+void SlotCache::hpush_tail(uint32_t k) {  // the least recently homed: the first to drop to its file
+  if (!c_.disk_tier) return;
+  Entry& x = e_[k];
+  x.hnext = kNil;
+  x.hprev = htail_;
+  if (htail_ != kNil) e_[htail_].hnext = k;
+  else hhead_ = k;
+  htail_ = k;
+  x.in_hlist = true;
+}
+
 std::vector<uint32_t> SlotCache::host_order() const {
   std::vector<uint32_t> out;
   for (uint32_t k = hhead_; k != kNil; k = e_[k].hnext) out.push_back(k);
@@ -212,7 +226,7 @@ std::vector<uint32_t> SlotCache::host_order() const {
 
 // A unit that leaves the device or a bank slot without a write-back: its block (a clean copy, or the block it was
 // served from) is its home again, else (file tier) its file.
-void SlotCache::to_lower(uint32_t k) {
+void SlotCache::to_lower(uint32_t k, bool cold) {
   Entry& x = e_[k];
   x.slot = -1;
   if (x.backed) {
@@ -221,7 +235,8 @@ void SlotCache::to_lower(uint32_t k) {
   }
   if (x.block >= 0) {
     x.home = Home::Host;
-    hpush(k);
+    if (cold) hpush_tail(k);
+    else hpush(k);
   } else {
     if (!c_.disk_tier) broken("a unit without a block left the device without a write-back");
     x.home = Home::File;
@@ -441,6 +456,7 @@ bool SlotCache::fetch(uint32_t g, uint32_t unit, bool prefetch) {
   const uint32_t k = key(g, unit);
   Entry& x = e_[k];
   if (prefetch && (pf_layer_[g] >= c_.prefetch_per_layer || pf_token_ >= c_.prefetch_per_token)) return false;
+  if (prefetch && c_.no_admit) return false;  // (no_admit issues no prefetch)
   switch (x.home) {
     case Home::Coming:
     case Home::Device:
@@ -487,18 +503,31 @@ bool SlotCache::fetch(uint32_t g, uint32_t unit, bool prefetch) {
       if (prefetch && !c_.disk_prefetch) return false;
       break;
   }
-  const size_t reserve = prefetch ? c_.prefetch_reserve : 0u;
-  if (free_slots_.size() <= reserve || (pressure_ && !prefetch)) st_.collected_mid += collect();
-  const bool capped = !prefetch && pressure_ && demand_free_used_ >= pressure_free_;
-  if (!prefetch && !capped && free_slots_.empty()) force_free_slot();
+  // a prefetch keeps the reserve free (pf_strict: the spare target's slots too)
+  const size_t reserve =
+      prefetch ? (c_.pf_strict ? std::max<size_t>(c_.prefetch_reserve, c_.spare_target) : c_.prefetch_reserve) : 0u;
   int32_t slot = -1;
   bool bank = false, free_counted = false;
-  if (!capped && free_slots_.size() > reserve) {
+  if (c_.no_admit) {  // a demand: its layer's bank slot, released at the boundary, its home unchanged
+    slot = bank_slot(g);
+    if (slot < 0)
+      fail(SS_E_BACKEND, "device-gated: dg_no_admit: no bank slot for a miss of gated layer " + std::to_string(g) +
+                             " (more distinct misses than dg_max_ids)");
+    bank = true;
+  } else if (free_slots_.size() <= reserve || (pressure_ && !prefetch)) {
+    st_.collected_mid += collect();
+  }
+  const bool capped = !prefetch && pressure_ && demand_free_used_ >= pressure_free_;
+  if (!bank && !prefetch && !capped && free_slots_.empty()) force_free_slot();
+  if (bank) {
+    // (no_admit: taken above)
+  } else if (!capped && free_slots_.size() > reserve) {
     if (!prefetch) ++demand_free_used_;
     free_counted = !prefetch;
     slot = free_slots_.back();
     free_slots_.pop_back();
   } else if (prefetch) {
+    if (c_.pf_strict && free_slots_.size() > c_.prefetch_reserve) ++st_.pf_strict_refused;
     return false;
   } else {
     slot = bank_slot(g);
@@ -690,9 +719,27 @@ void SlotCache::end_token(const std::vector<uint32_t>& keep, uint32_t rows) {
     for (uint32_t k : keep)
       if (k < keys_) kept[k] = 1;
   }
+  auto keep_k = [&](uint32_t k) { return !kept.empty() && kept[k]; };
   for (uint32_t k : coming_) {  // arrivals become device homes; their source blocks are free
     Entry& x = e_[k];
     if (x.home != Home::Coming) continue;
+    if (c_.pf_revert && x.via_pf && !x.used && !keep_k(k)) {
+      // an unused prefetch goes back: to its source block (still holding the bytes) at the pinned recency tail, or
+      // (read from it) to its file; no write-back, and the table upload below withdraws its entry
+      ++st_.pf_reverted;
+      st_.pf_revert_bytes += unit_bytes_;
+      free_slots_.push_back(x.slot);
+      to_lower(k, true);
+      table_[k] = -1;
+      unlink(k);
+      --on_device_;
+      x.via_pf = false;
+      if (x.pf_done) {
+        pool_.push_back(x.pf_done);
+        x.pf_done = nullptr;
+      }
+      continue;
+    }
     x.home = Home::Device;
     x.via_pf = false;
     if (x.pf_done) {
@@ -741,10 +788,12 @@ void SlotCache::end_token(const std::vector<uint32_t>& keep, uint32_t rows) {
   auto accept = [&](uint32_t k) {
     Entry& x = e_[k];
     // a clean copy (its block is its home again) or, file tier with no block to free, its file: no copy; a pinned
-    // unit dropped to its file frees a block first when none is free
-    if (x.backed || (free_blocks_.empty() && !drop_host_lru() && c_.disk_tier)) {
+    // unit dropped to its file frees a block first when none is free (clean_evict: none is dropped for it)
+    const bool clean = !x.backed && clean_now();
+    if (x.backed || clean || (free_blocks_.empty() && !drop_host_lru() && c_.disk_tier)) {
       if (x.backed) ++st_.inclusive_drops;
       else ++st_.disk_discards;
+      if (clean) count_clean();
       unlink(k);
       --on_device_;
       free_slots_.push_back(x.slot);
@@ -774,7 +823,8 @@ void SlotCache::end_token(const std::vector<uint32_t>& keep, uint32_t rows) {
   };
   // scored eviction: the lowest scores among the eligible units, when every gated layer was closed this token (a
   // layer the token did not export is closed here from its unchanged history); else the recency tail
-  const bool want_score = c_.scored && (!c_.scored_auto || rows > 1);
+  const bool select = !c_.no_admit;  // (no_admit: nothing was admitted, no boundary evicts)
+  const bool want_score = select && c_.scored && (!c_.scored_auto || rows > 1);
   for (uint32_t g = 0; c_.scored && g < gated(); ++g)
     if (!run_[g]) sc_[g].list_epoch = epoch_;
   bool by_score = want_score;
@@ -789,14 +839,14 @@ void SlotCache::end_token(const std::vector<uint32_t>& keep, uint32_t rows) {
     }
     st_.score_ns += uint64_t(
         std::chrono::duration_cast<std::chrono::nanoseconds>(std::chrono::steady_clock::now() - t0).count());
-  } else {
+  } else if (select) {
     for (uint32_t k = tail_; k != kNil && base + got < c_.spare_target;) {
       const uint32_t prev = e_[k].prev;
       if (eligible(k) && !accept(k)) break;
       k = prev;
     }
   }
-  if (pressure_ && pressure_recent_ && !short_blocks) {  // test pressure: the most recent ones too
+  if (select && pressure_ && pressure_recent_ && !short_blocks) {  // test pressure: the most recent ones too
     uint32_t n = 0;
     for (uint32_t k = head_; k != kNil && n < pressure_recent_;) {
       const uint32_t next = e_[k].next;
@@ -1160,13 +1210,15 @@ RoundOut SlotCache::round(const RoundIn& in, const std::vector<uint32_t>& kept_k
       const uint32_t v = dev[j];
       if (!(rs_[c] > in.hysteresis * rs_[v])) break;
       Entry& y = e_[v];
-      if (!fits(ub + (y.backed ? 0 : ub))) break;
+      const bool clean = !y.backed && clean_now();  // clean_evict: no free block, to its file (no write)
+      if (!fits(ub + (y.backed || clean ? 0 : ub))) break;
       const int32_t slot = y.slot;
-      if (y.backed) {  // a clean copy: its block is its home again, no write
+      if (y.backed || clean) {  // a clean copy: its block is its home again, no write (clean_evict: its file)
         unlink(v);
         --on_device_;
         table_[v] = -1;
         to_lower(v);
+        if (clean) count_clean();
       } else {
         const int32_t b = wb_block(c);
         if (b < 0) break;
@@ -1311,6 +1363,9 @@ void SlotCache::set_spare_target(uint32_t n) {
   c_.spare_target = n;
   if (c_.prefetch_reserve_auto) c_.prefetch_reserve = std::min<uint32_t>(24, n / 4);
 }
+
+void SlotCache::set_clean_evict(bool on) { c_.clean_evict = on; }
+void SlotCache::set_pf_revert(bool on) { c_.pf_revert = on; }
 
 void SlotCache::set_prefetch_budget(uint32_t per_layer, uint32_t per_token) {
   c_.prefetch_per_layer = per_layer;

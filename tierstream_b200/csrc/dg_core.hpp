@@ -106,6 +106,12 @@ struct CacheConfig {
   bool scored = false, scored_auto = false;
   uint32_t w_trans = 700, w_freq = 200, w_rec = 100;
   uint32_t max_ids = 64;
+  // The reference's opt-in policies: no_admit = every demand miss served through its layer's bank slot and released at
+  // the boundary (homes never change; no prefetch, no boundary eviction); clean_evict (file tier) = a victim that
+  // would need a block while none is free goes to its file with no copy, no pinned unit dropped for it; pf_revert = an
+  // unused prefetch goes back at the boundary (to its block at the pinned recency tail, or its file), not admitted;
+  // pf_strict = a prefetch also leaves the spare target's slots free.
+  bool no_admit = false, clean_evict = false, pf_revert = false, pf_strict = false;
 };
 
 struct CacheStats {
@@ -127,6 +133,9 @@ struct CacheStats {
   uint64_t score_ns = 0;
   // placement rounds: rounds run, units whose home they changed, bytes moved, host time, rounds cancelled
   uint64_t round_count = 0, round_units = 0, round_bytes = 0, round_ns = 0, round_cancelled = 0;
+  // opt-in policies: victims dropped to their file by clean_evict and their bytes; unused prefetches reverted and
+  // their bytes; prefetches pf_strict refused
+  uint64_t clean_drops = 0, clean_drop_bytes = 0, pf_reverted = 0, pf_revert_bytes = 0, pf_strict_refused = 0;
 };
 
 // A placement round's limits and what it did (ss_dg_round_params / ss_dg_round_result without the struct sizes).
@@ -235,6 +244,8 @@ class SlotCache {
   void set_spare_target(uint32_t n);
   void set_prefetch_budget(uint32_t per_layer, uint32_t per_token);
   void set_pressure(uint32_t free_per_token, uint32_t evict_recent);
+  void set_clean_evict(bool on);
+  void set_pf_revert(bool on);
   void set_mutation(int m) { mut_ = m; }
   // Every ownership rule (throws SS_E_BACKEND naming the first broken one).
   void check() const;
@@ -302,8 +313,14 @@ class SlotCache {
   void* finish_front();
   void force_free_slot();
   int32_t bank_slot(uint32_t g);
-  void to_lower(uint32_t k);
+  void to_lower(uint32_t k, bool cold = false);
   void hpush(uint32_t k);
+  void hpush_tail(uint32_t k);
+  bool clean_now() const { return c_.clean_evict && c_.disk_tier && free_blocks_.empty(); }
+  void count_clean() {
+    ++st_.clean_drops;
+    st_.clean_drop_bytes += unit_bytes_;
+  }
   void hunlink(uint32_t k);
   bool drop_host_lru();
   int32_t take_stage();

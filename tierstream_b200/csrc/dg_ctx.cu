@@ -142,8 +142,12 @@ Layout make_layout(const Desc& d, const Plan& p, const ss_options& o, const Peer
     refuse(SS_E_UNSUPPORTED, "dg_disk_queue above 1 (file reads in flight across calls) is not in this build: use 0 or 1 "
                              "(one read at a time inside its fetch)");
   if (o.dg_disk_tier && peer) refuse(SS_E_UNSUPPORTED, "the file tier with the peer tier is not in this build");
-  if (o.dg_no_admit || o.dg_clean_evict || o.dg_pf_revert_unused || o.dg_pf_strict_admit || o.dg_landing_blocks ||
-      o.dg_bank_keep || o.dg_disk_queue_adapt || o.dg_prior_len)
+  // the reference's opt-in policies this build has (dg_layout.cpp:208-215)
+  if (o.dg_no_admit > 1) refuse(SS_E_INVALID, "dg_no_admit must be 0 or 1");
+  if (o.dg_clean_evict > 1) refuse(SS_E_INVALID, "dg_clean_evict must be 0 or 1");
+  if (o.dg_pf_revert_unused > 1) refuse(SS_E_INVALID, "dg_pf_revert_unused must be 0 or 1");
+  if (o.dg_pf_strict_admit > 1) refuse(SS_E_INVALID, "dg_pf_strict_admit must be 0 or 1");
+  if (o.dg_landing_blocks || o.dg_bank_keep || o.dg_disk_queue_adapt || o.dg_prior_len)
     refuse(SS_E_UNSUPPORTED, "an opt-in device-gated policy of the reference that is not in this build is set");
   Layout x;
   x.B = o.dg_max_ids;
@@ -1140,6 +1144,11 @@ class CudaDgContext final : public DgContext {
     s.round_bytes = d(c.round_bytes, base_.round_bytes);
     s.round_ns = d(c.round_ns, base_.round_ns);
     s.round_cancelled = d(c.round_cancelled, base_.round_cancelled);
+    s.clean_drops = d(c.clean_drops, base_.clean_drops);
+    s.clean_drop_bytes = d(c.clean_drop_bytes, base_.clean_drop_bytes);
+    s.pf_reverted = d(c.pf_reverted, base_.pf_reverted);
+    s.pf_revert_bytes = d(c.pf_revert_bytes, base_.pf_revert_bytes);
+    s.pf_strict_refused = d(c.pf_strict_refused, base_.pf_strict_refused);
     s.disk_queue_resolved = x_.disk_tier ? 1u : 0u;
     std::memcpy(out, &s, sizeof s);
   }
@@ -1239,6 +1248,16 @@ class CudaDgContext final : public DgContext {
   }
   const RoundOut& last_round() const override { return core_->last_round(); }
   void round_cancel() override { core_->cancel_round(); }
+  void set_clean_evict(uint32_t on) override {
+    require(!in_token_, SS_E_INVALID, "ss_dg_set_clean_evict: between tokens only");
+    require(on <= 1, SS_E_INVALID, "ss_dg_set_clean_evict: 0 or 1");
+    core_->set_clean_evict(on != 0);
+  }
+  void set_pf_revert_unused(uint32_t on) override {
+    require(!in_token_, SS_E_INVALID, "ss_dg_set_pf_revert_unused: between tokens only");
+    require(on <= 1, SS_E_INVALID, "ss_dg_set_pf_revert_unused: 0 or 1");
+    core_->set_pf_revert(on != 0);
+  }
   void round_seed_counts(const ss_dg_unit* units, const float* counts, uint32_t n) override {
     require(!in_token_, SS_E_INVALID, "ss_dg_round_seed_counts: between tokens only");
     std::vector<uint32_t> keys;
@@ -1513,6 +1532,10 @@ class CudaDgContext final : public DgContext {
     c.w_freq = x_.w_freq;
     c.w_rec = x_.w_rec;
     c.max_ids = x_.B;
+    c.no_admit = o_.dg_no_admit != 0;  // (the banks hold dg_max_ids each: the layout checked the ring)
+    c.clean_evict = o_.dg_clean_evict != 0;  // (no effect without the file tier)
+    c.pf_revert = o_.dg_pf_revert_unused != 0;
+    c.pf_strict = o_.dg_pf_strict_admit != 0;
     if (x_.disk_tier) {  // a file miss: the unit's parts from their files, checked against the descriptor's hash
       unsigned n = 8;
       if (const char* e = std::getenv("TSB_FILE_READERS")) n = unsigned(std::max(1L, std::min(64L, std::atol(e))));

@@ -111,6 +111,10 @@ void dg_replay(const tsb_dg_replay_config* c, const int32_t* ids, const int32_t*
     cfg.w_rec = c->w_rec;
   }
   cfg.max_ids = c->n_ids;
+  cfg.no_admit = c->no_admit != 0;
+  cfg.clean_evict = c->clean_evict != 0;
+  cfg.pf_revert = c->pf_revert != 0;
+  cfg.pf_strict = c->pf_strict != 0;
   uint32_t keys = 0;
   for (uint32_t g = 0; g < c->n_gated; ++g) keys += c->n_units[g];
   HostMover m(std::vector<uint64_t>(c->part_bytes, c->part_bytes + c->n_parts), keys,
@@ -180,6 +184,11 @@ void dg_replay(const tsb_dg_replay_config* c, const int32_t* ids, const int32_t*
       rsum[5] += r.bytes_read + r.bytes_h2d + r.bytes_written_back;
     }
     if (c->rstats) std::memcpy(c->rstats + size_t(t) * 6, rsum, sizeof rsum);
+    if (c->pstats) {
+      const CacheStats& q = core.stats();
+      const uint64_t pv[5] = {q.clean_drops, q.clean_drop_bytes, q.pf_reverted, q.pf_revert_bytes, q.pf_strict_refused};
+      std::memcpy(c->pstats + size_t(t) * 5, pv, sizeof pv);
+    }
     std::memcpy(tables + size_t(t) * keys, m.table_.data(), size_t(keys) * 4);
     const CacheStats& s = core.stats();
     const uint64_t v[16] = {s.tokens,        s.lookups,     s.misses,          s.covered,     s.fetched,
