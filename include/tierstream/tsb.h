@@ -102,6 +102,10 @@ typedef struct tsb_dg_replay_config {
    * (optional): [tokens][5] clean_drops, clean_drop_bytes, pf_reverted, pf_revert_bytes, pf_strict_refused */
   uint32_t no_admit, clean_evict, pf_revert, pf_strict;
   uint64_t* pstats;
+  /* file tier: reads in flight at once (0 / 1 = each inside its fetch); qstats (optional): [tokens][4]
+   * disk_overlapped, disk_max_in_flight, disk_carried, disk_carried_bytes */
+  uint32_t disk_queue, reserved3;
+  uint64_t* qstats;
 } tsb_dg_replay_config;
 SS_API ss_status tsb_test_dg_replay(const tsb_dg_replay_config* cfg, const int32_t* ids, const int32_t* preds,
                                     int32_t* tables, uint64_t* stats, const uint8_t* src_units, uint64_t* read_sum);

@@ -47,6 +47,10 @@ typedef struct oref_dg_config {
    * pf_revert_bytes, pf_strict_refused */
   uint32_t no_admit, clean_evict, pf_revert, pf_strict;
   uint64_t* pstats;
+  /* three-tier reads in flight (0 / 1 = synchronous); qstats (optional): [tokens][4] disk_overlapped,
+   * disk_max_in_flight, disk_carried, disk_carried_bytes */
+  uint32_t disk_queue, reserved3;
+  uint64_t* qstats;
 } oref_dg_config;
 #define OREF_NXSTATS 6
 

@@ -141,7 +141,7 @@ extern "C" __attribute__((visibility("default"))) int oref_dg_replay(const oref_
     cfg.disk_prefetch = c->disk_prefetch != 0;
     cfg.home_blocks = c->home_blocks;
     cfg.disk_staging = c->disk_staging;
-    cfg.disk_queue = 1;  // synchronous reads
+    cfg.disk_queue = c->disk_queue ? c->disk_queue : 1;  // (its transport's begin is the synchronous read)
     cfg.scored = c->policy != 0;  // the bounded boundary selection, as its device-gated context configures it
     cfg.scored_auto = c->policy == 2;
     cfg.boundary_score = true;
@@ -207,7 +207,7 @@ extern "C" __attribute__((visibility("default"))) int oref_dg_replay(const oref_
           core.serve_prediction(g + 1, pred.data(), c->n_pred, c->n_ids, false);
         }
         if (core.deferred() && g + 1 < c->n_gated) core.issue_writebacks(g, [] { return false; });
-        core.score_layer(g);  // (the service closes each layer after its work)
+        if (core.scored()) core.score_layer(g);  // (the service closes each layer after its work, scored only)
       }
       core.end_token({}, c->rows ? c->rows : 1);
       if (c->reset_at && tok + 1 == c->reset_at) core.reset_open();
@@ -226,6 +226,11 @@ extern "C" __attribute__((visibility("default"))) int oref_dg_replay(const oref_
         rsum[5] += r.bytes_read + r.bytes_h2d + r.bytes_written_back;
       }
       if (c->rstats) std::memcpy(c->rstats + size_t(tok) * 6, rsum, sizeof rsum);
+      if (c->qstats) {
+        const ts::DgStats& q = core.stats();
+        const uint64_t qv[4] = {q.disk_overlapped, q.disk_max_in_flight, q.disk_carried, q.disk_carried_bytes};
+        std::memcpy(c->qstats + size_t(tok) * 4, qv, sizeof qv);
+      }
       if (c->pstats) {
         const ts::DgStats& q = core.stats();
         const uint64_t pv[5] = {q.clean_drops, q.clean_drop_bytes, q.pf_reverted, q.pf_revert_bytes,

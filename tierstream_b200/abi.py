@@ -146,7 +146,8 @@ class dg_replay_config(C.Structure):
                 ("profile", C.POINTER(u32)), ("round_every", u32), ("round_max_units", u32),
                 ("round_hysteresis", C.c_float), ("round_decay", C.c_float), ("round_budget", u64),
                 ("rstats", C.POINTER(u64)), ("no_admit", u32), ("clean_evict", u32), ("pf_revert", u32),
-                ("pf_strict", u32), ("pstats", C.POINTER(u64))]
+                ("pf_strict", u32), ("pstats", C.POINTER(u64)), ("disk_queue", u32), ("reserved3", u32),
+                ("qstats", C.POINTER(u64))]
 
 
 class ss_dg_round_params(C.Structure):

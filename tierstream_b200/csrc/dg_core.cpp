@@ -69,6 +69,12 @@ SlotCache::SlotCache(const CacheConfig& cfg, Mover* m) : c_(cfg), m_(m) {
 }
 
 SlotCache::~SlotCache() {
+  for (const Pending& p : pending_) {  // reads in flight end before anything they write into can be freed
+    try {
+      m_->read_end(p.handle);
+    } catch (...) {
+    }
+  }
   for (void* ev : all_events_) m_->event_destroy(ev);
 }
 
@@ -105,6 +111,7 @@ void SlotCache::apply_wb_defer() {
 }
 
 void SlotCache::place(const std::vector<uint32_t>& order, const std::vector<uint8_t>* disk) {
+  drain_pending();
   const uint32_t dev_max = c_.persistent_slots - c_.spare_target;
   std::vector<uint8_t> taken(keys_, 0);
   std::vector<uint32_t> dev;
@@ -258,15 +265,153 @@ bool SlotCache::drop_host_lru() {
   return true;
 }
 
-// The next staging buffer in rotation, once its last copy landed.
+// The next staging buffer in rotation, once a read still holding it ended and its last copy landed.
 int32_t SlotCache::take_stage() {
   const uint32_t i = stage_next_;
   stage_next_ = (i + 1) % c_.disk_staging;
+  const int32_t block = int32_t(c_.blocks + i);
+  end_reads([block](const Pending& p) { return p.stage == block; });
   if (stage_ev_[i] && !m_->done(stage_ev_[i])) {
     m_->event_sync(stage_ev_[i]);
     ++st_.disk_stage_waits;
   }
-  return int32_t(c_.blocks + i);
+  return block;
+}
+
+// ---- file reads in flight (disk_queue > 1) ----
+// A file miss's fetch takes its slot and staging buffer and changes every host record at once (homes, the table
+// mirror, lists, counters); only the device work that needs the bytes waits for the read's end: its copy, its entry,
+// the staging buffer's event and a prefetch's event. Reads end at drain points: the demand reads at every public entry
+// point, a key's read when the key is touched again, the reads a layer routes before its ready, a staging buffer's read
+// before its reuse, the oldest when the queue is full, every read at the boundary and at any setting.
+void SlotCache::enter() {
+  ++entries_;
+  drain_demand();
+}
+
+void SlotCache::drain_pending(size_t n) {
+  end_reads([&n](const Pending&) {
+    if (n == 0) return false;
+    --n;
+    return true;
+  });
+}
+
+void SlotCache::drain_demand() {
+  end_reads([](const Pending& p) { return !p.prefetch; });
+}
+
+void SlotCache::drain_key(uint32_t k) {
+  end_reads([k](const Pending& p) { return p.key == k; });
+}
+
+// The demand reads and the prefetch reads of units layer g routes (a wrong prediction's read keeps running).
+void SlotCache::drain_layer(uint32_t g, const uint32_t* ids, uint32_t n) {
+  const uint32_t first = key(g, 0);
+  end_reads([this, g, ids, n, first](const Pending& p) {
+    return !p.prefetch || (gated_of(p.key) == g && std::find(ids, ids + n, p.key - first) != ids + n);
+  });
+}
+
+// The picked records leave pending_ (the others keep their order) and end oldest first. A read that failed is undone
+// (its key back in its file, its slot back); after a failed copy every record left is undone and nothing more is
+// enqueued. The first failure is rethrown.
+void SlotCache::end_reads(const std::function<bool(const Pending&)>& pick) {
+  if (pending_.empty()) return;
+  std::vector<uint8_t> picked(pending_.size());
+  for (size_t i = 0; i < pending_.size(); ++i) picked[i] = pick(pending_[i]) ? 1 : 0;
+  std::vector<Pending> ending;
+  ending.reserve(pending_.size());
+  size_t kept = 0;
+  for (size_t i = 0; i < pending_.size(); ++i) {
+    if (picked[i]) ending.push_back(pending_[i]);
+    else pending_[kept++] = pending_[i];
+  }
+  pending_.resize(kept);
+  std::exception_ptr first;
+  bool device_failed = false;
+  for (size_t i = 0; i < ending.size(); ++i) {
+    const Pending p = ending[i];
+    if (p.entry != entries_) {  // it ran while its fetch's caller went on
+      ++st_.disk_carried;
+      st_.disk_carried_bytes += unit_bytes_;
+    }
+    const auto t0 = std::chrono::steady_clock::now();
+    bool read_ok = true;
+    try {
+      st_.disk_read_ns += m_->read_end(p.handle);
+    } catch (...) {
+      read_ok = false;
+      if (!first) first = std::current_exception();
+    }
+    st_.disk_wait_ns += uint64_t(
+        std::chrono::duration_cast<std::chrono::nanoseconds>(std::chrono::steady_clock::now() - t0).count());
+    if (!read_ok || device_failed) {
+      undo_pending(p);
+      continue;
+    }
+    ++st_.disk_reads;
+    st_.disk_read_bytes += unit_bytes_;
+    try {
+      finish_pending(p);
+    } catch (...) {
+      if (!first) first = std::current_exception();
+      device_failed = true;  // (this record stays fetched, as a synchronous fetch whose copy failed)
+      ending.insert(ending.end(), pending_.begin(), pending_.end());
+      pending_.clear();
+    }
+  }
+  if (first) std::rethrow_exception(first);
+}
+
+// An ended read's device work: the copy from its staging buffer and the entry, the buffer's event, a prefetch's event.
+void SlotCache::finish_pending(const Pending& p) {
+  Entry& x = e_[p.key];
+  if (mut_ == kEntryBeforeCopy) {  // test-only fault: the entry before its bytes
+    publish(p.s, p.key, p.slot);
+    m_->h2d(p.s, p.slot, p.stage, p.key);
+  } else {
+    m_->h2d(p.s, p.slot, p.stage, p.key);
+    publish(p.s, p.key, p.slot);
+  }
+  void*& ev = stage_ev_[uint32_t(p.stage) - c_.blocks];  // the staging buffer is reusable once this copy landed
+  if (!ev) ev = event();
+  m_->record(ev, p.s);
+  if (p.prefetch) {
+    x.pf_done = event();
+    m_->record(x.pf_done, p.s);
+  }
+}
+
+// A read that failed: the key goes back to its file, its slot to where it came from (a bank slot stays used for the
+// layer, unpublished); nothing was enqueued for it.
+void SlotCache::undo_pending(const Pending& p) {
+  Entry& x = e_[p.key];
+  const uint32_t g = gated_of(p.key);
+  table_[p.key] = -1;
+  if (p.bank) {
+    bank_key_[size_t(p.slot) - bank_first_] = kNil;
+    banked_.erase(std::find(banked_.begin(), banked_.end(), p.key));
+    --st_.bank_serves;
+    --lc_[g].bank_serves;
+  } else {
+    unlink(p.key);
+    --on_device_;
+    coming_.erase(std::find(coming_.begin(), coming_.end(), p.key));
+    free_slots_.push_back(p.slot);
+    if (p.free_counted) --demand_free_used_;
+  }
+  x.home = Home::File;
+  x.slot = -1;
+  x.via_pf = x.used = false;
+  ++on_file_;
+  if (p.prefetch) {
+    --st_.prefetched;
+    --lc_[g].prefetched;
+  } else {
+    --st_.fetched;
+    --lc_[g].fetched;
+  }
 }
 
 // ---- the recency list (head = most recently used) ----
@@ -371,6 +516,7 @@ void* SlotCache::finish_front() {
 }
 
 void SlotCache::issue_writebacks(uint32_t g, const std::function<bool()>& ahead) {
+  enter();
   if (deferred_.empty()) {
     credit_ = 0;
     return;
@@ -427,6 +573,7 @@ int32_t SlotCache::bank_slot(uint32_t g) {
   const int32_t slot = int32_t(bank_first_ + idx);
   const uint32_t old = bank_key_[idx];
   if (old != kNil && e_[old].home == Home::Bank && e_[old].slot == slot) {
+    drain_key(old);  // (its read, were it still in flight, ends before the alias goes)
     to_lower(old);  // its block, or (read from it) its file
     publish(Mover::kDem, old, -1);
   }
@@ -436,6 +583,7 @@ int32_t SlotCache::bank_slot(uint32_t g) {
 
 void SlotCache::begin_token(uint32_t seq, const std::vector<uint8_t>* run) {
   require(!run || run->size() == gated(), SS_E_INVALID, "device-gated: the exported layers do not cover the gated layers");
+  enter();
   if (run) std::copy(run->begin(), run->end(), run_.begin());
   else std::fill(run_.begin(), run_.end(), uint8_t(1));
   if (c_.scored) {  // the token's epoch (the first is 1); one token cannot push more than 2^40 stamps
@@ -459,6 +607,8 @@ bool SlotCache::fetch(uint32_t g, uint32_t unit, bool prefetch) {
   if (prefetch && c_.no_admit) return false;  // (no_admit issues no prefetch)
   switch (x.home) {
     case Home::Coming:
+      drain_key(k);  // (its own prefetch read in flight: ended)
+      return false;
     case Home::Device:
     case Home::Bank:
       return false;
@@ -534,6 +684,7 @@ bool SlotCache::fetch(uint32_t g, uint32_t unit, bool prefetch) {
     if (slot >= 0) {
       bank = true;
     } else {  // more distinct misses than a bank holds: only an internal error gets here
+      drain_pending();
       force_free_slot();
       while (free_slots_.empty() && !wbs_.empty()) {
         m_->event_sync(wbs_.front().done);
@@ -547,44 +698,52 @@ bool SlotCache::fetch(uint32_t g, uint32_t unit, bool prefetch) {
   }
   const Mover::Stream s = prefetch ? Mover::kPf : Mover::kDem;
   const bool from_file = x.home == Home::File;
-  int32_t src = x.block;
-  if (from_file) {  // its bytes from the file into a staging buffer, then the same copy
-    const int32_t stage = take_stage();
-    const auto t0 = std::chrono::steady_clock::now();
+  if (from_file) {  // its bytes from the file into a staging buffer, then the same copy once the read ended
+    const size_t depth = std::max<uint32_t>(c_.disk_queue, 1);
     try {
-      m_->read_unit(k, stage);
-    } catch (...) {  // nothing enqueued for this key: its slot goes back (a bank slot stays used, unpublished)
+      if (pending_.size() >= depth) {  // a full queue: the completed reads, then the oldest demand reads, then the oldest
+        end_reads([this](const Pending& p) { return m_->read_done(p.handle); });
+        if (pending_.size() >= depth) {
+          size_t n = pending_.size() + 1 - depth;
+          end_reads([&n](const Pending& p) {
+            if (n == 0 || p.prefetch) return false;
+            --n;
+            return true;
+          });
+        }
+        if (pending_.size() >= depth) drain_pending(pending_.size() + 1 - depth);
+      }
+      const int32_t stage = take_stage();
+      const auto t0 = std::chrono::steady_clock::now();
+      void* h = m_->read_begin(k, stage);
+      st_.disk_read_ns += uint64_t(
+          std::chrono::duration_cast<std::chrono::nanoseconds>(std::chrono::steady_clock::now() - t0).count());
+      if (!pending_.empty()) ++st_.disk_overlapped;
+      pending_.push_back({k, slot, stage, s, prefetch, bank, free_counted, h, entries_});
+      st_.disk_max_in_flight = std::max<uint64_t>(st_.disk_max_in_flight, pending_.size());
+    } catch (...) {  // nothing begun for this key: its slot goes back (a bank slot stays used, unpublished)
       if (!bank) {
         free_slots_.push_back(slot);
         if (free_counted) --demand_free_used_;
       }
       throw;
     }
-    st_.disk_read_ns += uint64_t(
-        std::chrono::duration_cast<std::chrono::nanoseconds>(std::chrono::steady_clock::now() - t0).count());
-    ++st_.disk_reads;
-    st_.disk_read_bytes += unit_bytes_;
-    src = stage;
-  }
-  if (mut_ == kEntryBeforeCopy) {  // test-only fault: the entry before its bytes
-    publish(s, k, slot);
-    m_->h2d(s, slot, src, k);
-  } else {
-    m_->h2d(s, slot, src, k);
-    publish(s, k, slot);
-  }
-  if (from_file) {  // the staging buffer is reusable once this copy landed
-    void*& ev = stage_ev_[uint32_t(src) - c_.blocks];
-    if (!ev) ev = event();
-    m_->record(ev, s);
+    table_[k] = slot;  // the mirror now; the device's entry with the copy
     --on_file_;
   } else {
+    if (mut_ == kEntryBeforeCopy) {  // test-only fault: the entry before its bytes
+      publish(s, k, slot);
+      m_->h2d(s, slot, x.block, k);
+    } else {
+      m_->h2d(s, slot, x.block, k);
+      publish(s, k, slot);
+    }
     hunlink(k);  // (a Host unit: out of the pinned recency list)
   }
   x.slot = slot;
   x.via_pf = prefetch;
   x.used = false;
-  if (prefetch) {
+  if (prefetch && !from_file) {  // (a file read's: with its copy)
     x.pf_done = event();
     m_->record(x.pf_done, s);
   }
@@ -609,11 +768,15 @@ bool SlotCache::fetch(uint32_t g, uint32_t unit, bool prefetch) {
     ++st_.fetched;
     ++lc_[g].fetched;
   }
+  if (from_file && c_.disk_queue <= 1) drain_pending();  // synchronous reads: the copy now
   return true;
 }
 
 void SlotCache::cover(uint32_t g, uint32_t unit) {
   Entry& x = e_[key(g, unit)];
+  // only this key's copy lands before the ready: its read ends first if in flight (a file prefetch's event comes
+  // with its copy), the wait is on its own event
+  if (x.home == Home::Coming && x.via_pf && mut_ != kNoCover) drain_key(key(g, unit));
   if (x.home == Home::Coming && x.via_pf && x.pf_done && mut_ != kNoCover) {
     m_->wait(Mover::kDem, x.pf_done);
     ++st_.covered_waits;
@@ -621,6 +784,7 @@ void SlotCache::cover(uint32_t g, uint32_t unit) {
 }
 
 void SlotCache::use(uint32_t g, uint32_t unit, bool was_miss) {
+  enter();
   const uint32_t k = key(g, unit);
   Entry& x = e_[k];
   ++st_.lookups;
@@ -646,6 +810,7 @@ void SlotCache::use(uint32_t g, uint32_t unit, bool was_miss) {
 }
 
 void SlotCache::serve_demand(uint32_t g, const uint32_t* ids, uint32_t n, uint64_t mask) {
+  enter();
   const uint32_t nu = units(g);
   for (uint32_t i = 0; i < n; ++i)
     require(ids[i] < nu, SS_E_INVALID,
@@ -663,13 +828,16 @@ void SlotCache::serve_demand(uint32_t g, const uint32_t* ids, uint32_t n, uint64
       fetch(g, ids[i], false);
     }
   }
+  drain_layer(g, ids, n);  // this layer's copies and entries (its demand reads, the prefetch reads it routes)
   if (mask) {
+    drain_demand();  // (the ready follows every demand read's copy and entry)
     m_->ready(g, seq_);
     m_->diag_mark(g, 1);
   }
 }
 
 void SlotCache::serve_use(uint32_t g, const uint32_t* ids, uint32_t n, uint64_t mask) {
+  enter();
   const bool have_pred = pred_layer_ == g;
   uniq_.assign(ids, ids + n);
   std::sort(uniq_.begin(), uniq_.end());
@@ -694,6 +862,7 @@ void SlotCache::serve_use(uint32_t g, const uint32_t* ids, uint32_t n, uint64_t 
 // device running ahead does not skip it (the reference's default prediction admission).
 void SlotCache::serve_prediction(uint32_t g_next, const uint32_t* pred, uint32_t n, bool ahead) {
   (void)ahead;
+  enter();  // (its prefetches' file reads stay in flight past the call)
   if (g_next >= gated()) return;
   const uint32_t nu = units(g_next);
   uniq_.clear();
@@ -711,6 +880,7 @@ void SlotCache::serve_prediction(uint32_t g_next, const uint32_t* pred, uint32_t
 }
 
 void SlotCache::end_token(const std::vector<uint32_t>& keep, uint32_t rows) {
+  drain_pending();  // the end of the token: no read in flight while its streams sync and victims are chosen
   m_->sync(Mover::kDem);
   m_->sync(Mover::kPf);
   std::vector<uint8_t> kept;
@@ -925,6 +1095,7 @@ void SlotCache::score_history(uint32_t g) {
 }
 
 void SlotCache::score_layer(uint32_t g) {
+  enter();
   if (!c_.scored || g >= gated() || sc_[g].served != epoch_) return;  // (not served: the boundary falls back)
   sc_[g].list_epoch = epoch_;
 }
@@ -1000,6 +1171,7 @@ void SlotCache::reset_score() {
 void SlotCache::set_policy(uint32_t policy) {
   require(policy <= 2, SS_E_INVALID, "device-gated: policy must be LRU, SCORED or SCORED_AUTO");
   require(!policy || !sc_.empty(), SS_E_INVALID, "device-gated: scoring must be provisioned at open");
+  drain_pending();
   drain();
   collect();
   c_.scored = policy != 0;
@@ -1308,6 +1480,7 @@ void SlotCache::seed_round_counts(const std::vector<uint32_t>& keys, const std::
 }
 
 uint32_t SlotCache::seed(const std::vector<uint32_t>& keys) {
+  drain_pending();  // between tokens (copies, then an upload)
   stamp_room("ss_seed");
   if (!coming_.empty()) m_->sync(Mover::kPf);
   collect();
@@ -1334,6 +1507,7 @@ uint32_t SlotCache::seed(const std::vector<uint32_t>& keys) {
 }
 
 void SlotCache::drain() {
+  drain_pending();
   while (!deferred_.empty()) finish_front();
   m_->sync(Mover::kDem);
   m_->sync(Mover::kPf);
@@ -1349,6 +1523,7 @@ std::vector<uint32_t> SlotCache::residency() const {
 }
 
 void SlotCache::set_wb_defer(bool on) {
+  drain_pending();  // (settings: between tokens, every read ended first)
   if (on == c_.wb_defer) return;
   if (!on)
     while (!deferred_.empty()) finish_front();
@@ -1359,20 +1534,29 @@ void SlotCache::set_wb_defer(bool on) {
 }
 
 void SlotCache::set_spare_target(uint32_t n) {
+  drain_pending();
   require(n <= c_.persistent_slots, SS_E_INVALID, "device-gated: spare target above the persistent slots");
   c_.spare_target = n;
   if (c_.prefetch_reserve_auto) c_.prefetch_reserve = std::min<uint32_t>(24, n / 4);
 }
 
-void SlotCache::set_clean_evict(bool on) { c_.clean_evict = on; }
-void SlotCache::set_pf_revert(bool on) { c_.pf_revert = on; }
+void SlotCache::set_clean_evict(bool on) {
+  drain_pending();
+  c_.clean_evict = on;
+}
+void SlotCache::set_pf_revert(bool on) {
+  drain_pending();
+  c_.pf_revert = on;
+}
 
 void SlotCache::set_prefetch_budget(uint32_t per_layer, uint32_t per_token) {
+  drain_pending();
   c_.prefetch_per_layer = per_layer;
   c_.prefetch_per_token = per_token;
 }
 
 void SlotCache::set_pressure(uint32_t free_per_token, uint32_t evict_recent) {
+  drain_pending();
   pressure_ = free_per_token != 0 || evict_recent != 0;
   pressure_free_ = free_per_token;
   pressure_recent_ = evict_recent;

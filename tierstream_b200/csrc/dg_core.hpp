@@ -64,6 +64,21 @@ class Mover {
   // File tier: every part of unit `key` from its file into `block` (blocks [blocks, blocks + disk_staging) are the
   // staging buffers, -1 the reset staging buffer), synchronously; no copy reads the block meanwhile.
   virtual void read_unit(uint32_t key, int32_t block);
+  // The same read in flight (disk_queue > 1): begin starts it and returns a handle; end waits for it, rethrows its
+  // failure and returns its own read time in ns (0: begin was the read); done answers without waiting. Every begun
+  // read is ended once. Default: begin is the synchronous read.
+  virtual void* read_begin(uint32_t key, int32_t block) {
+    read_unit(key, block);
+    return nullptr;
+  }
+  virtual uint64_t read_end(void* handle) {
+    (void)handle;
+    return 0;
+  }
+  virtual bool read_done(void* handle) {
+    (void)handle;
+    return true;
+  }
   // slot_of[key] = v after everything enqueued on s so far (a release at system scope).
   virtual void publish(Stream s, uint32_t key, int32_t v) = 0;
   // ready[g] = seq on kDem after everything enqueued there.
@@ -100,6 +115,10 @@ struct CacheConfig {
   // File tier (dg_disk_tier): see the file comment. disk_prefetch: predictions may read file-homed units too.
   bool disk_tier = false, disk_prefetch = false;
   uint32_t home_blocks = 0, disk_staging = 0;
+  // file reads in flight at once (1 = each read inside its fetch): a read's copy and entry follow when it ends, at the
+  // first drain point that needs it (its key touched again, its layer's ready, its staging buffer reused, a full queue,
+  // the boundary); a prefetch's read may stay in flight across the service's calls
+  uint32_t disk_queue = 1;
   // Scored eviction: the history is kept from the open when `scored` (the tables exist only then); scored_auto takes
   // scored victims only after a boundary of more than one row. Weights out of 1000 (sum 1000); max_ids = the most ids
   // one export holds (a union's bound).
@@ -127,6 +146,9 @@ struct CacheStats {
   // buffer's last copy; pinned units dropped to their file to free a block; victims dropped to their file
   uint64_t disk_reads = 0, disk_read_bytes = 0, disk_read_ns = 0, disk_stage_waits = 0, disk_drops = 0;
   uint64_t disk_discards = 0;
+  // reads begun while another was in flight, the most in flight at once, reads ended in a later public call than
+  // their fetch's and their bytes, the wall time spent waiting for reads to end
+  uint64_t disk_overlapped = 0, disk_max_in_flight = 0, disk_carried = 0, disk_carried_bytes = 0, disk_wait_ns = 0;
   // scored eviction: boundaries that fell back to the recency order (a layer without this token's ranking), victims
   // taken by score, layers scored and the candidates they ranked, saturated transition increments, selection time
   uint64_t score_fallbacks = 0, scored_victims = 0, score_layers = 0, score_candidates = 0, score_saturated = 0;
@@ -279,6 +301,23 @@ class SlotCache {
 
   void unlink(uint32_t k);
   void push_front(uint32_t k);
+  // ---- file reads in flight ----
+  struct Pending {
+    uint32_t key;
+    int32_t slot, stage;
+    Mover::Stream s;
+    bool prefetch, bank, free_counted;  // free_counted: a demand that took a free slot (demand_free_used_)
+    void* handle;
+    uint64_t entry;  // the public call that began it
+  };
+  void enter();  // a public entry point: the demand reads end
+  void end_reads(const std::function<bool(const Pending&)>& pick);
+  void drain_pending(size_t n = SIZE_MAX);
+  void drain_demand();
+  void drain_key(uint32_t k);
+  void drain_layer(uint32_t g, const uint32_t* ids, uint32_t n);
+  void finish_pending(const Pending& p);
+  void undo_pending(const Pending& p);
   // ---- scored eviction ----
   struct ScoreCand {
     uint64_t s, epoch, stamp;
@@ -343,6 +382,8 @@ class SlotCache {
   uint32_t hhead_ = kNil, htail_ = kNil, on_file_ = 0, open_hhead_ = kNil, open_htail_ = kNil, open_on_file_ = 0;
   uint32_t stage_next_ = 0;
   std::vector<void*> stage_ev_;  // per staging buffer: its last copy's event
+  std::vector<Pending> pending_;  // file reads in flight, oldest first
+  uint64_t entries_ = 0;          // public calls so far (a read ended in a later one was carried)
   std::vector<LayerScore> sc_;
   std::vector<uint8_t> run_;
   uint64_t epoch_ = 0, stamp_ = 0, open_stamp_ = 0;

@@ -741,7 +741,7 @@ class Service {
       }
       if (core_->deferred() && nx < G)
         core_->issue_writebacks(g, [&] { return !deterministic_ && load_acquire(&m_.flag[nx]) == seq; });
-      core_->score_layer(g);  // scored eviction: layer g's union, epochs and stamps are final for this token
+      if (core_->scored()) core_->score_layer(g);  // scored eviction: layer g is final for this token
       const auto t_end = Clock::now();
       t.serve_us = us_between(t_seen, t_end);
       if (diag_) {

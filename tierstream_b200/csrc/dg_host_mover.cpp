@@ -102,6 +102,7 @@ void dg_replay(const tsb_dg_replay_config* c, const int32_t* ids, const int32_t*
   cfg.disk_prefetch = c->disk_prefetch != 0;
   cfg.home_blocks = c->home_blocks;
   cfg.disk_staging = c->disk_staging;
+  cfg.disk_queue = c->disk_queue ? c->disk_queue : 1;
   require(c->policy <= 2, SS_E_INVALID, "tsb_test_dg_replay: policy 0..2");
   cfg.scored = c->policy != 0;
   cfg.scored_auto = c->policy == 2;
@@ -165,7 +166,7 @@ void dg_replay(const tsb_dg_replay_config* c, const int32_t* ids, const int32_t*
         core.serve_prediction(g + 1, pred.data(), c->n_pred, false);
       }
       if (core.deferred() && g + 1 < c->n_gated) core.issue_writebacks(g, [] { return false; });
-      core.score_layer(g);
+      if (core.scored()) core.score_layer(g);  // (the service closes a layer for scoring only)
     }
     core.end_token({}, c->rows ? c->rows : 1);
     if (c->reset_at && t + 1 == c->reset_at) core.reset_open();
@@ -184,6 +185,11 @@ void dg_replay(const tsb_dg_replay_config* c, const int32_t* ids, const int32_t*
       rsum[5] += r.bytes_read + r.bytes_h2d + r.bytes_written_back;
     }
     if (c->rstats) std::memcpy(c->rstats + size_t(t) * 6, rsum, sizeof rsum);
+    if (c->qstats) {
+      const CacheStats& q = core.stats();
+      const uint64_t qv[4] = {q.disk_overlapped, q.disk_max_in_flight, q.disk_carried, q.disk_carried_bytes};
+      std::memcpy(c->qstats + size_t(t) * 4, qv, sizeof qv);
+    }
     if (c->pstats) {
       const CacheStats& q = core.stats();
       const uint64_t pv[5] = {q.clean_drops, q.clean_drop_bytes, q.pf_reverted, q.pf_revert_bytes, q.pf_strict_refused};
