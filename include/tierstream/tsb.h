@@ -125,6 +125,12 @@ SS_API ss_status tsb_test_host_locs(ss_ctx* c, int layer, int32_t* out, int n);
 SS_API ss_status tsb_test_file_read(const char* path, uint64_t offset, uint64_t bytes, void* dst, uint64_t piece,
                                     uint32_t threads, int direct);
 
+/* Test hook: n reads of `bytes` bytes at offsets[i] of the file at `path` into dst + i x bytes, all begun at once on
+ * `threads` reader threads (the file tier's reads in flight), then ended in order (or in reverse); the first failure is
+ * returned after every read ended. */
+SS_API ss_status tsb_test_async_reads(const char* path, const uint64_t* offsets, uint32_t n, uint64_t bytes, void* dst,
+                                      uint32_t threads, int reverse);
+
 /* Test hooks of scored eviction's profile (the reference's TSSCPRF1 format, ss.h "Scored eviction"): the SHA-256 of
  * len bytes into out[32]; the profile identity of d's gated layers (every layer with units) into identity[32] and,
  * when profile is given, every rule of the format checked (SS_E_INVALID naming the first one broken) and its counts

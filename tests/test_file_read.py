@@ -45,3 +45,35 @@ def test_read_past_the_end_fails(data_file):
     st = abi.load().tsb_test_file_read(path.encode(), data.size - 100, 8192, out.ctypes.data, 4096, 2, 1)
     assert st == abi.SS_E_IO
     assert st == abi.load().tsb_test_file_read(os.devnull.encode() + b"-missing", 0, 1, out.ctypes.data, 1, 1, 0)
+
+
+@pytest.mark.parametrize("threads,reverse", [(1, 0), (3, 0), (4, 1), (8, 1)])
+def test_reads_in_flight_equal_the_file(data_file, threads, reverse):
+    """The file tier's reads in flight (dg_disk_queue > 1): many reads begun at once on a few reader threads and ended
+    in order or in reverse each land their own bytes."""
+    path, data = data_file
+    rng = np.random.default_rng(threads)
+    n, size = 24, 256 << 10
+    offs = (rng.integers(0, (data.size - size) // 4096, size=n) * 4096).astype(np.uint64)
+    buf = mmap.mmap(-1, n * size)
+    base = C.addressof(C.c_char.from_buffer(buf))
+    abi.check(abi.load().tsb_test_async_reads(path.encode(), offs.ctypes.data_as(C.POINTER(C.c_uint64)), n, size, base,
+                                              threads, reverse))
+    got = np.frombuffer(buf, dtype=np.uint8, count=n * size).reshape(n, size)
+    for i in range(n):
+        assert np.array_equal(got[i], data[int(offs[i]):int(offs[i]) + size]), i
+    del got
+    buf.close()
+
+
+def test_a_failed_read_in_flight_is_reported_after_all_ended(data_file):
+    path, data = data_file
+    offs = np.array([0, data.size + 4096, 8192], dtype=np.uint64)  # the second one reads past the end
+    out = mmap.mmap(-1, 3 * 4096)
+    base = C.addressof(C.c_char.from_buffer(out))
+    st = abi.load().tsb_test_async_reads(path.encode(), offs.ctypes.data_as(C.POINTER(C.c_uint64)), 3, 4096, base, 2, 0)
+    assert st == abi.SS_E_IO
+    got = np.frombuffer(out, dtype=np.uint8, count=3 * 4096)
+    assert np.array_equal(got[:4096], data[:4096]) and np.array_equal(got[8192:], data[8192:12288])
+    del got
+    out.close()

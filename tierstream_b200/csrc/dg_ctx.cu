@@ -22,6 +22,8 @@
 #include <cstring>
 #include <functional>
 #include <memory>
+#include <condition_variable>
+#include <deque>
 #include <mutex>
 #include <thread>
 
@@ -105,7 +107,7 @@ struct Layout {
   std::vector<uint32_t> residents;  // keys of tier R, key order
   // file tier (dg_disk_tier): F units of tier DISK (flagged per key in `disk`), S staging buffers after the blocks
   bool disk_tier = false, disk_prefetch = false;
-  uint32_t F = 0, S = 0;
+  uint32_t F = 0, S = 0, disk_queue = 0;
   std::vector<uint8_t> disk;
   // scored eviction (SS_POLICY_SCORED / SCORED_AUTO): the weights and a profile's counts (empty: none)
   bool scored = false, scored_auto = false;
@@ -131,16 +133,14 @@ Layout make_layout(const Desc& d, const Plan& p, const ss_options& o, const Peer
   if (o.dg_wait_timeout_ms < 1) refuse(SS_E_INVALID, "dg_wait_timeout_ms must be >= 1");
   if (o.dg_wb_defer > 1) refuse(SS_E_INVALID, "dg_wb_defer must be 0 or 1");
   if (o.dg_wb_stream > 1) refuse(SS_E_INVALID, "dg_wb_stream must be 0 or 1");
-  // the file tier with synchronous reads (dg_disk_queue 0 or 1), as the reference checks its options
-  // (dg_layout.cpp:200-207); a read queue (> 1 or SS_DG_DISK_QUEUE_AUTO) is not in this build
+  // the file tier, as the reference checks its options (dg_layout.cpp:200-207)
   constexpr uint32_t kQueueAuto = 0xFFFFFFFFu;
   if (o.dg_disk_tier > 1 || o.dg_disk_prefetch > 1) refuse(SS_E_INVALID, "dg_disk_tier / dg_disk_prefetch must be 0 or 1");
   if (!o.dg_disk_tier && (o.dg_disk_prefetch || o.dg_disk_staging || (o.dg_disk_queue && o.dg_disk_queue != kQueueAuto)))
     refuse(SS_E_INVALID, "dg_disk_prefetch / dg_disk_staging / dg_disk_queue need dg_disk_tier = 1");
   if (o.dg_disk_staging > 256) refuse(SS_E_INVALID, "dg_disk_staging must be 0..256");
-  if (o.dg_disk_tier && o.dg_disk_queue > 1)
-    refuse(SS_E_UNSUPPORTED, "dg_disk_queue above 1 (file reads in flight across calls) is not in this build: use 0 or 1 "
-                             "(one read at a time inside its fetch)");
+  if (o.dg_disk_queue > 64 && o.dg_disk_queue != kQueueAuto)
+    refuse(SS_E_INVALID, "dg_disk_queue must be 0..64 or SS_DG_DISK_QUEUE_AUTO");
   if (o.dg_disk_tier && peer) refuse(SS_E_UNSUPPORTED, "the file tier with the peer tier is not in this build");
   // the reference's opt-in policies this build has (dg_layout.cpp:208-215)
   if (o.dg_no_admit > 1) refuse(SS_E_INVALID, "dg_no_admit must be 0 or 1");
@@ -212,7 +212,16 @@ Layout make_layout(const Desc& d, const Plan& p, const ss_options& o, const Peer
   x.R = uint32_t(x.residents.size());
   x.disk_tier = o.dg_disk_tier != 0;
   x.disk_prefetch = o.dg_disk_prefetch != 0;
-  x.S = x.disk_tier ? (o.dg_disk_staging ? o.dg_disk_staging : 8u) : 0u;
+  // reads in flight and staging buffers, resolved as the reference resolves them (dg_layout.cpp:159-181): AUTO is
+  // clamp(3 x locations, 4, 8) bounded by an explicit staging count (one location per source here: no stripes), the
+  // staging default 8 raised to it; an explicit queue 0 means 1
+  if (x.disk_tier && o.dg_disk_queue == kQueueAuto) {
+    x.disk_queue = o.dg_disk_staging ? std::min<uint32_t>(4, o.dg_disk_staging) : 4u;
+    x.S = o.dg_disk_staging ? o.dg_disk_staging : std::max<uint32_t>(8, x.disk_queue);
+  } else if (x.disk_tier) {
+    x.disk_queue = o.dg_disk_queue ? o.dg_disk_queue : 1u;
+    x.S = o.dg_disk_staging ? o.dg_disk_staging : 8u;
+  }
   // scored eviction: the weights, the per-layer bound and the profile (every rule of its format, against this
   // descriptor's identity), as the reference resolves them (dg_layout.cpp:349-371)
   if (o.policy == SS_POLICY_SCORED || o.policy == SS_POLICY_SCORED_AUTO) {
@@ -420,6 +429,16 @@ class CudaMover final : public Mover {
     reader_(key, block_host(block));
   }
   void set_reader(std::function<void(uint32_t, char*)> f) { reader_ = std::move(f); }
+  void set_async(AsyncReads* a) { async_ = a; }
+  void* read_begin(uint32_t key, int32_t block) override {
+    if (!async_) {
+      read_unit(key, block);
+      return nullptr;
+    }
+    return async_->begin(key, block_host(block));
+  }
+  uint64_t read_end(void* h) override { return async_ && h ? async_->end(h) : 0; }
+  bool read_done(void* h) override { return !async_ || !h || async_->done(h); }
   void h2h(int32_t src, int32_t dst, uint32_t key) override {
     if (peer_ && peer_->owned(key)) return;
     std::memcpy(block_host(dst), block_host(src), size_t(x_.unit_bytes));
@@ -565,6 +584,7 @@ class CudaMover final : public Mover {
   Buffers b_;
   const PeerTier* peer_ = nullptr;
   std::function<void(uint32_t, char*)> reader_;
+  AsyncReads* async_ = nullptr;
   uint64_t peer_units_ = 0, self_units_ = 0;
   cudaStream_t s_[3] = {nullptr, nullptr, nullptr};
   int32_t* table_pin_ = nullptr;
@@ -1127,12 +1147,15 @@ class CudaDgContext final : public DgContext {
     s.disk_reads = d(c.disk_reads, base_.disk_reads);
     s.disk_read_bytes = d(c.disk_read_bytes, base_.disk_read_bytes);
     s.disk_read_ns = d(c.disk_read_ns, base_.disk_read_ns);
-    s.disk_wait_ns = s.disk_read_ns;  // synchronous reads: the service waits for each one whole
+    s.disk_wait_ns = d(c.disk_wait_ns, base_.disk_wait_ns);
     s.disk_stage_waits = d(c.disk_stage_waits, base_.disk_stage_waits);
     s.disk_drops = d(c.disk_drops, base_.disk_drops);
     s.disk_discards = d(c.disk_discards, base_.disk_discards);
     s.disk_units = core_->file_units();
-    s.disk_max_in_flight = c.disk_reads ? 1 : 0;  // (a gauge since open: one read at a time)
+    s.disk_max_in_flight = c.disk_max_in_flight;  // (a gauge since open)
+    s.disk_overlapped = d(c.disk_overlapped, base_.disk_overlapped);
+    s.disk_carried = d(c.disk_carried, base_.disk_carried);
+    s.disk_carried_bytes = d(c.disk_carried_bytes, base_.disk_carried_bytes);
     s.score_fallbacks = d(c.score_fallbacks, base_.score_fallbacks);
     s.scored_victims = d(c.scored_victims, base_.scored_victims);
     s.score_layers = d(c.score_layers, base_.score_layers);
@@ -1149,7 +1172,8 @@ class CudaDgContext final : public DgContext {
     s.pf_reverted = d(c.pf_reverted, base_.pf_reverted);
     s.pf_revert_bytes = d(c.pf_revert_bytes, base_.pf_revert_bytes);
     s.pf_strict_refused = d(c.pf_strict_refused, base_.pf_strict_refused);
-    s.disk_queue_resolved = x_.disk_tier ? 1u : 0u;
+    s.disk_queue_resolved = x_.disk_queue;
+    s.disk_locations = x_.disk_tier && o_.dg_disk_queue == 0xFFFFFFFFu ? 1u : 0u;
     std::memcpy(out, &s, sizeof s);
   }
   void layer_stats(int layer, ss_layer_stats* out) const override {
@@ -1369,7 +1393,7 @@ class CudaDgContext final : public DgContext {
   // A file-tier read: the unit's parts in pieces of at most 8 MiB, read by the reader pool at once (the reference
   // reads a unit in one pass on one reader); with verify_hash and descriptor hashes, the bytes are checked on the host
   // before any copy reads them (the reference's read_checked, dg_ctx.cpp:1625-1633).
-  void read_checked(int layer, int unit, char* dst) const {
+  void read_checked(int layer, int unit, char* dst, bool pooled = true) const {
     const Layer& l = d_.layers[size_t(layer)];
     struct Piece {
       const SourceFile* f;
@@ -1384,7 +1408,11 @@ class CudaDgContext final : public DgContext {
         pieces.push_back({files_[size_t(p.source)].get(), base + o, std::min(kReadPiece, p.bytes - o), dst + at + o});
       at += p.bytes;
     }
-    readers_->run(pieces.size(), [&](size_t i) { pieces[i].f->read(pieces[i].dst, pieces[i].off, pieces[i].bytes); });
+    if (pooled) {
+      readers_->run(pieces.size(), [&](size_t i) { pieces[i].f->read(pieces[i].dst, pieces[i].off, pieces[i].bytes); });
+    } else {  // (a read in flight: on its own reader thread, piece after piece)
+      for (const Piece& q : pieces) q.f->read(q.dst, q.off, q.bytes);
+    }
     if (o_.verify_hash && !l.hash.empty())
       require(xxh64(dst, size_t(x_.unit_bytes)) == l.hash[size_t(unit)], SS_E_HASH,
               "device-gated: unit (" + std::to_string(layer) + ", " + std::to_string(unit) +
@@ -1526,6 +1554,7 @@ class CudaDgContext final : public DgContext {
     c.disk_prefetch = x_.disk_prefetch;
     c.home_blocks = x_.disk_tier ? x_.P : 0;  // the plan's pinned units get the blocks; the rest are spares
     c.disk_staging = x_.S;
+    c.disk_queue = std::max<uint32_t>(1, x_.disk_queue);
     c.scored = x_.scored;
     c.scored_auto = x_.scored_auto;
     c.w_trans = x_.w_trans;
@@ -1545,6 +1574,14 @@ class CudaDgContext final : public DgContext {
                                     x_.unit_base.begin()) - 1;
         read_checked(x_.gated[g], int(key - x_.unit_base[g]), dst);
       });
+      if (x_.disk_queue > 1) {  // reads in flight: one reader thread per read the queue holds
+        async_ = std::make_unique<AsyncReads>(x_.disk_queue, [this](uint32_t key, char* dst) {
+          const uint32_t g = uint32_t(std::upper_bound(x_.unit_base.begin(), x_.unit_base.end(), key) -
+                                      x_.unit_base.begin()) - 1;
+          read_checked(x_.gated[g], int(key - x_.unit_base[g]), dst, false);
+        });
+        mover_->set_async(async_.get());
+      }
     }
     core_ = std::make_unique<SlotCache>(c, mover_.get());
     std::vector<uint32_t> order;
@@ -1727,6 +1764,7 @@ class CudaDgContext final : public DgContext {
     svc_.reset();
     core_.reset();
     mover_.reset();
+    async_.reset();
     readers_.reset();
     for (char* a : bufs_.arena) cudaFree(a);
     if (bufs_.slot_of) cudaFree(bufs_.slot_of);
@@ -1746,6 +1784,7 @@ class CudaDgContext final : public DgContext {
   std::vector<std::unique_ptr<SourceFile>> files_;
   static constexpr uint64_t kReadPiece = uint64_t(8) << 20;  // file tier: the reader pool's piece
   std::unique_ptr<ReadPool> readers_;                        // file tier: the reads of one miss at once
+  std::unique_ptr<AsyncReads> async_;                        // file tier: reads in flight (dg_disk_queue > 1)
   CudaMover::Buffers bufs_;
   uint32_t* ctl_ = nullptr;
   void* mapped_h_ = nullptr;

@@ -6,6 +6,7 @@
 
 #include <algorithm>
 #include <cerrno>
+#include <chrono>
 #include <cstdlib>
 #include <cstring>
 #include <memory>
@@ -104,6 +105,79 @@ void SourceFile::read(void* dst, uint64_t offset, uint64_t bytes) const {
     out += want;
     pos += want;
     left -= want;
+  }
+}
+
+AsyncReads::AsyncReads(unsigned threads, std::function<void(uint32_t, char*)> read) : read_(std::move(read)) {
+  for (unsigned i = 0; i < std::max(1u, threads); ++i) th_.emplace_back([this] { loop(); });
+}
+
+AsyncReads::~AsyncReads() {
+  {
+    std::lock_guard<std::mutex> lk(mu_);
+    stop_ = true;
+  }
+  cv_.notify_all();
+  for (std::thread& t : th_) t.join();
+  for (Job* j : running_) delete j;
+  for (size_t i = head_; i < q_.size(); ++i) delete q_[i];
+}
+
+void* AsyncReads::begin(uint32_t key, char* dst) {
+  Job* j = new Job;
+  j->key = key;
+  j->dst = dst;
+  {
+    std::lock_guard<std::mutex> lk(mu_);
+    q_.push_back(j);
+  }
+  cv_.notify_one();
+  return j;
+}
+
+bool AsyncReads::done(void* h) const { return static_cast<const Job*>(h)->done.load(std::memory_order_acquire); }
+
+uint64_t AsyncReads::end(void* h) {
+  Job* j = static_cast<Job*>(h);
+  {
+    std::unique_lock<std::mutex> lk(mu_);
+    done_cv_.wait(lk, [&] { return j->done.load(std::memory_order_acquire); });
+    auto it = std::find(running_.begin(), running_.end(), j);
+    require(it != running_.end(), SS_E_BACKEND, "a file read ended twice");
+    running_.erase(it);
+  }
+  std::unique_ptr<Job> own(j);
+  if (j->err) std::rethrow_exception(j->err);
+  return j->ns;
+}
+
+void AsyncReads::loop() {
+  for (;;) {
+    Job* j = nullptr;
+    {
+      std::unique_lock<std::mutex> lk(mu_);
+      cv_.wait(lk, [&] { return stop_ || head_ < q_.size(); });
+      if (head_ == q_.size()) return;  // (stopping with nothing queued)
+      j = q_[head_++];
+      if (head_ == q_.size()) {  // the queue's storage reused once every job was taken
+        q_.clear();
+        head_ = 0;
+      }
+      running_.push_back(j);
+    }
+    const auto t0 = std::chrono::steady_clock::now();
+    try {
+      read_(j->key, j->dst);
+    } catch (...) {
+      j->err = std::current_exception();
+    }
+    j->ns = uint64_t(
+        std::chrono::duration_cast<std::chrono::nanoseconds>(std::chrono::steady_clock::now() - t0).count());
+    {
+      std::lock_guard<std::mutex> lk(mu_);
+      j->done.store(true, std::memory_order_release);
+    }
+    done_cv_.notify_all();
   }
 }
 

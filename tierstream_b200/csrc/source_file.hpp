@@ -17,6 +17,39 @@ namespace tsb {
 
 // A fixed set of reader threads serving one job at a time: run(n, fn) calls fn(i) for every i in [0, n) on the
 // threads and the caller, returns once all calls finished and rethrows the first failure. One caller at a time.
+// Reads in flight: a fixed set of reader threads, one read each at a time, oldest first. begin queues read(key, dst)
+// and returns its handle; done answers without waiting; end waits for it, rethrows its failure and returns its time in
+// ns. Every begun read must be ended exactly once, before the destination is reused or freed; queued reads still run
+// at destruction.
+class AsyncReads {
+ public:
+  AsyncReads(unsigned threads, std::function<void(uint32_t, char*)> read);
+  ~AsyncReads();
+  AsyncReads(const AsyncReads&) = delete;
+  AsyncReads& operator=(const AsyncReads&) = delete;
+  void* begin(uint32_t key, char* dst);
+  bool done(void* h) const;
+  uint64_t end(void* h);
+
+ private:
+  struct Job {
+    uint32_t key = 0;
+    char* dst = nullptr;
+    std::atomic<bool> done{false};
+    std::exception_ptr err;
+    uint64_t ns = 0;
+  };
+  void loop();
+  std::function<void(uint32_t, char*)> read_;
+  std::mutex mu_;
+  std::condition_variable cv_, done_cv_;
+  std::vector<Job*> q_;                    // queued, oldest first (owned)
+  std::vector<Job*> running_;              // taken by a reader, not yet ended (owned)
+  size_t head_ = 0;                        // the next queued job
+  std::vector<std::thread> th_;
+  bool stop_ = false;
+};
+
 class ReadPool {
  public:
   explicit ReadPool(unsigned threads);

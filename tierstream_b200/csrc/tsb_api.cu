@@ -154,6 +154,28 @@ ss_status tsb_test_file_read(const char* path, uint64_t offset, uint64_t bytes, 
   });
 }
 
+ss_status tsb_test_async_reads(const char* path, const uint64_t* offsets, uint32_t n, uint64_t bytes, void* dst,
+                               uint32_t threads, int reverse) {
+  return run([&] {
+    tsb::require(path && (offsets || !n) && (dst || !n) && threads >= 1 && threads <= 64, SS_E_INVALID,
+                 "tsb_test_async_reads: bad argument");
+    tsb::SourceFile f(path, 4096, true);
+    tsb::AsyncReads q(threads, [&](uint32_t i, char* out) { f.read(out, offsets[i], bytes); });
+    std::vector<void*> h(n);
+    for (uint32_t i = 0; i < n; ++i) h[i] = q.begin(i, static_cast<char*>(dst) + uint64_t(i) * bytes);
+    std::exception_ptr first;
+    for (uint32_t k = 0; k < n; ++k) {
+      const uint32_t i = reverse ? n - 1 - k : k;
+      try {
+        q.end(h[i]);
+      } catch (...) {
+        if (!first) first = std::current_exception();
+      }
+    }
+    if (first) std::rethrow_exception(first);
+  });
+}
+
 uint64_t tsb_xxh64(const void* data, size_t len, uint64_t seed) { return tsb::xxh64(data, len, seed); }
 
 int tsb_cuda_arch(void) { return 100; }
