@@ -131,6 +131,18 @@ SS_API ss_status tsb_test_file_read(const char* path, uint64_t offset, uint64_t 
 SS_API ss_status tsb_test_async_reads(const char* path, const uint64_t* offsets, uint32_t n, uint64_t bytes, void* dst,
                                       uint32_t threads, int reverse);
 
+/* Test hook: a host-mode resident set (one layer) driven as the host forward mode drives it: n_place units placed at
+ * the open (place_pin: pinned), then per step the routed units routed[step][k] (-1 = none) with flags[step][unit]
+ * (bit 0: busy, in flight; bit 1: prefetched this forward, so neither a hit nor admitted, a miss for recency), one
+ * admission (admit_misses[step], max_ev[step] evictions at most, -1 = no cap) and one observation. Outputs per step:
+ * slots_out[step][unit] (-1 = not resident) and counts_out[step][5] (hits, admitted, evicted, transient, deferred).
+ * policy: 0 LRU, 1 SCORED with `window` forwards of frequency. */
+SS_API ss_status tsb_test_resident_replay(int32_t n_units, int32_t capacity, int32_t policy, uint32_t window,
+                                         const int32_t* place_units, const uint8_t* place_pin, uint32_t n_place,
+                                         uint32_t steps, const int32_t* routed, uint32_t k, const uint8_t* flags,
+                                         const int32_t* max_ev, const uint8_t* admit_misses, int32_t* slots_out,
+                                         int32_t* counts_out);
+
 /* Test hooks of scored eviction's profile (the reference's TSSCPRF1 format, ss.h "Scored eviction"): the SHA-256 of
  * len bytes into out[32]; the profile identity of d's gated layers (every layer with units) into identity[32] and,
  * when profile is given, every rule of the format checked (SS_E_INVALID naming the first one broken) and its counts

@@ -12,6 +12,7 @@
 #include <list>
 #include <memory>
 #include <mutex>
+#include <stdexcept>
 #include <string>
 #include <thread>
 #include <vector>
@@ -124,4 +125,65 @@ extern "C" __attribute__((visibility("default"))) int oref_host_replay(
   ss_plan_free(p);
   ss_desc_free(d);
   return 0;
+}
+
+// The reference's own ResidentSet (resident_set.cpp) driven the way its host forward mode's ingest drives it
+// (stream_ctx.cpp:1303-1354), for the resident-set parity test.
+namespace {
+void req(bool ok, const char* what) {
+  if (!ok) throw std::runtime_error(what);
+}
+}  // namespace
+extern "C" __attribute__((visibility("default"))) int oref_resident_replay(
+    int32_t n_units, int32_t capacity, int32_t policy, uint32_t window, const int32_t* place_units,
+    const uint8_t* place_pin, uint32_t n_place, uint32_t steps, const int32_t* routed, uint32_t k,
+    const uint8_t* flags, const int32_t* max_ev, const uint8_t* admit_misses, int32_t* slots_out, int32_t* counts_out,
+    char* err, size_t errlen) {
+  using RS = ts::ResidentSet;
+
+  try {
+    req(n_units > 0 && capacity >= 0 && (policy == 0 || policy == 1) && (place_units || !n_place) &&
+             (routed || !steps || !k) && flags && max_ev && admit_misses && slots_out && counts_out,
+         "resident replay: bad argument");
+    RS rs(n_units, capacity, policy == 1 ? SS_POLICY_SCORED : SS_POLICY_LRU, window);
+    for (uint32_t i = 0; i < n_place; ++i) rs.place(place_units[i], place_pin && place_pin[i]);
+    for (uint32_t t = 0; t < steps; ++t) {
+      std::vector<char> count(size_t(n_units), 0), busy(size_t(n_units), 0);
+      for (uint32_t i = 0; i < k; ++i) {
+        const int32_t u = routed[size_t(t) * k + i];
+        req(u < n_units, "resident replay: unit out of range");
+        if (u >= 0) count[size_t(u)] = 1;
+      }
+      const uint8_t* f = flags + size_t(t) * size_t(n_units);
+      std::vector<int32_t> routed_now, misses, to_admit;
+      int hits = 0;
+      for (int32_t u = 0; u < n_units; ++u) {  // the host forward mode's ingest order
+        if (f[u] & 1) busy[size_t(u)] = 1;
+        if (!count[size_t(u)]) continue;
+        busy[size_t(u)] = 1;
+        routed_now.push_back(u);
+        if (f[u] & 2) {
+          misses.push_back(u);
+        } else if (rs.slot(u) >= 0) {
+          ++hits;
+        } else {
+          to_admit.push_back(u);
+          misses.push_back(u);
+        }
+      }
+      const auto a = rs.admit(to_admit, busy, admit_misses[t] != 0, max_ev[t]);
+      rs.observe(routed_now, misses);
+      for (int32_t u = 0; u < n_units; ++u) slots_out[size_t(t) * size_t(n_units) + size_t(u)] = rs.slot(u);
+      int32_t* c = counts_out + size_t(t) * 5;
+      c[0] = hits;
+      c[1] = int32_t(a.admitted.size());
+      c[2] = int32_t(a.evicted.size());
+      c[3] = int32_t(a.transient.size());
+      c[4] = a.deferred;
+    }
+    return 0;
+  } catch (const std::exception& e) {
+    if (err && errlen) std::snprintf(err, errlen, "%s", e.what());
+    return -1;
+  }
 }

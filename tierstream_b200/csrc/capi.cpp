@@ -14,6 +14,7 @@
 #include "json.hpp"
 #include "peer.hpp"
 #include "plan.hpp"
+#include "resident_set.hpp"
 #include "score_profile.hpp"
 #include "strix_stream/ss.h"
 #include "strix_stream/ss_test.h"
@@ -338,7 +339,8 @@ ss_status open_impl(const ss_desc* d, const ss_budget* budget, const ss_plan* pl
       *out = new ss_ctx{nullptr, std::move(dg)};
     } else {
       need(!peer, "tsb_open_peer: the peer tier serves device-gated decode only (forward_mode DEVICE_GATED)");
-      need(o.policy == SS_POLICY_LRU, "ss_open: host mode supports SS_POLICY_LRU in this build");
+      need(o.policy != SS_POLICY_SCORED_AUTO, "ss_open: SCORED_AUTO needs device-gated mode");
+      need(o.policy == SS_POLICY_LRU || o.policy == SS_POLICY_SCORED, "ss_open: policy must be LRU or SCORED");
       auto h = tsb::open_host_context(d->d, bb, p, o);
       *out = new ss_ctx{std::move(h), nullptr};
     }
@@ -658,6 +660,54 @@ ss_status tsb_peer_index(const int32_t* owner, uint32_t keys, uint32_t world, in
     const std::vector<int64_t> ix = tsb::store_index(std::vector<int32_t>(owner, owner + keys), world, &per);
     if (index) std::copy(ix.begin(), ix.end(), index);
     if (units_per_rank) std::copy(per.begin(), per.end(), units_per_rank);
+  });
+}
+
+ss_status tsb_test_resident_replay(int32_t n_units, int32_t capacity, int32_t policy, uint32_t window,
+                                  const int32_t* place_units, const uint8_t* place_pin, uint32_t n_place, uint32_t steps,
+                                  const int32_t* routed, uint32_t k, const uint8_t* flags, const int32_t* max_ev,
+                                  const uint8_t* admit_misses, int32_t* slots_out, int32_t* counts_out) {
+  using RS = tsb::ResidentSet;
+  return guard([&] {
+    need(n_units > 0 && capacity >= 0 && (policy == 0 || policy == 1) && (place_units || !n_place) &&
+             (routed || !steps || !k) && flags && max_ev && admit_misses && slots_out && counts_out,
+         "resident replay: bad argument");
+    RS rs(n_units, capacity, policy == 1, window);
+    for (uint32_t i = 0; i < n_place; ++i) rs.place(place_units[i], place_pin && place_pin[i]);
+    for (uint32_t t = 0; t < steps; ++t) {
+      std::vector<char> count(size_t(n_units), 0), busy(size_t(n_units), 0);
+      for (uint32_t i = 0; i < k; ++i) {
+        const int32_t u = routed[size_t(t) * k + i];
+        need(u < n_units, "resident replay: unit out of range");
+        if (u >= 0) count[size_t(u)] = 1;
+      }
+      const uint8_t* f = flags + size_t(t) * size_t(n_units);
+      std::vector<int32_t> routed_now, misses, to_admit;
+      int hits = 0;
+      for (int32_t u = 0; u < n_units; ++u) {  // the host forward mode's ingest order
+        if (f[u] & 1) busy[size_t(u)] = 1;
+        if (!count[size_t(u)]) continue;
+        busy[size_t(u)] = 1;
+        routed_now.push_back(u);
+        if (f[u] & 2) {
+          misses.push_back(u);
+        } else if (rs.slot(u) >= 0) {
+          ++hits;
+        } else {
+          to_admit.push_back(u);
+          misses.push_back(u);
+        }
+      }
+      const auto a = rs.admit(to_admit, busy, admit_misses[t] != 0, max_ev[t]);
+      rs.observe(routed_now, misses);
+      for (int32_t u = 0; u < n_units; ++u) slots_out[size_t(t) * size_t(n_units) + size_t(u)] = rs.slot(u);
+      int32_t* c = counts_out + size_t(t) * 5;
+      c[0] = hits;
+      c[1] = int32_t(a.admitted.size());
+      c[2] = int32_t(a.evicted.size());
+      c[3] = int32_t(a.transient.size());
+      c[4] = a.deferred;
+    }
   });
 }
 

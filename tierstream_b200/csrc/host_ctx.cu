@@ -899,7 +899,7 @@ class HostCtx final : public HostContext {
     for (int i = 0; i < n; ++i)
       if (ids[i] >= 0) ++s.count[size_t(ids[i])];
     ss_layer_stats& st = fwd_[size_t(layer)];
-    std::vector<int32_t> to_admit;
+    std::vector<int32_t> to_admit, misses;  // misses: prefetched this forward or not resident (SCORED's recency)
     std::vector<char> busy(size_t(l.n_units), 0);
     for (int u = 0; u < l.n_units; ++u) {
       if (s.loc[size_t(u)] != kNone) busy[size_t(u)] = 1;
@@ -914,10 +914,13 @@ class HostCtx final : public HostContext {
         } else {
           ++st.prefetched;
         }
+        misses.push_back(u);
       } else if (s.rs->slot(u) >= 0) {
         s.hits.push_back(u);
+      } else {
+        to_admit.push_back(u);
+        misses.push_back(u);
       }
-      else to_admit.push_back(u);
     }
     st.routed += s.routed.size();
     st.hits += s.hits.size();
@@ -933,7 +936,7 @@ class HostCtx final : public HostContext {
     st.admitted += a.admitted.size();
     st.transient += a.transient.size();
     st.evicted += a.evicted.size();
-    s.rs->observe(s.routed);
+    s.rs->observe(s.routed, misses);
   }
 
   void init() {
@@ -1042,7 +1045,7 @@ class HostCtx final : public HostContext {
         if (t == SS_TIER_RESIDENT || t == SS_TIER_RESIDENT_BACKED) ++planned;
       }
       const int cap = l.streamable ? std::min(l.n_units, planned + int(plan_.dynamic_slots_per_layer)) : l.n_units;
-      s.rs = std::make_unique<ResidentSet>(l.n_units, cap);
+      s.rs = std::make_unique<ResidentSet>(l.n_units, cap, o_.policy == SS_POLICY_SCORED, o_.score_window);
       if (cap) {
         void* p = nullptr;
         ck(cudaMalloc(&p, size_t(uint64_t(cap) * stride(int(L)))), "cudaMalloc (pool)");
