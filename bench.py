@@ -73,6 +73,12 @@ def args_():
     p.add_argument("--pinned-per-layer", type=int, default=0,
                    help="file tier: non-resident experts per layer that keep a pinned block (the rest in the file)")
     p.add_argument("--staging", type=int, default=4, help="file tier: staging buffers (ss_options.dg_disk_staging)")
+    p.add_argument("--disk-queue", type=int, default=0,
+                   help="file tier: file reads in flight (ss_options.dg_disk_queue; 0 / 1 = each inside its fetch)")
+    p.add_argument("--policy", default="lru", choices=["lru", "scored", "scored_auto"],
+                   help="device-gated eviction policy (ss_options.policy)")
+    p.add_argument("--round-every", type=int, default=0,
+                   help="a placement round (ss_dg_round, defaults) after every N tokens, inside the timed steps")
     p.add_argument("--workload", default="mixtral-8x7b-dg", choices=["mixtral-8x7b-dg", "qwen3-235b-a22b-peer"],
                    help="mixtral-8x7b-dg: BASELINE configs[1] (default); qwen3-235b-a22b-peer: configs[4], the peer "
                         "tier on 4 or more GPUs")
@@ -357,7 +363,8 @@ def main():
     run = harness.DgRun(model, resident_keys=resident_keys(1 + rank), spare_per_layer=a.spare, max_ids=TOP_K,
                         diag=True, test_hooks=False, mode=1, slices=128, wb_defer=a.wb_defer, wb_stream=a.wb_stream,
                         inclusive=inclusive, peer=setup.tier if setup else None,
-                        disk_keys=disk_keys(a, resident_keys(1)) if a.file else (), disk_staging=a.staging)
+                        disk_keys=disk_keys(a, resident_keys(1)) if a.file else (), disk_staging=a.staging,
+                        disk_queue=a.disk_queue, policy={"lru": 0, "scored": 1, "scored_auto": 2}[a.policy])
     t_open = time.perf_counter() - t_open
     unit = model.unit_bytes
     try:
@@ -380,6 +387,8 @@ def main():
                 run.ids_dev.copy_(trace_dev[t], non_blocking=True)
                 run.graph.launch()
             run.ctx.end()
+            if a.round_every and (t + 1) % a.round_every == 0:
+                run.ctx.round()
         e1.record(run.stream)
         e1.synchronize()
         barrier()
@@ -402,6 +411,8 @@ def main():
         w0 = time.perf_counter()
         for t in range(a.steps):
             run.step(ids2[t])
+            if a.round_every and (t + 1) % a.round_every == 0:
+                run.ctx.round()
         w1 = time.perf_counter()
         barrier()
         s3 = run.ctx.stats()
@@ -413,7 +424,9 @@ def main():
                                          "writebacks_done", "collected_mid", "wb_forced", "wb_forced_wait_ns",
                                          "wb_boundary_flushed", "wb_deferred", "wb_cancelled", "resurrected",
                                          "wb_issued_bytes", "covered", "disk_reads", "disk_read_bytes",
-                                         "disk_read_ns", "disk_drops", "disk_discards")}
+                                         "disk_read_ns", "disk_drops", "disk_discards", "disk_overlapped",
+                                         "disk_carried", "scored_victims", "score_fallbacks", "round_count",
+                                         "round_units", "round_bytes")}
         full = json.loads(run.ctx.stats_json())
         peer_stats, open_stats = full["peer"], full["open"]
     finally:
@@ -465,7 +478,8 @@ def main():
         "gpu_launches": int(a.steps * (2 + 2 * LAYERS) + land_launches + a.steps * LAYERS),
         "clocks": clk, "open_s": round(t_open, 2), "open": open_stats, "dg": dg, "miss_layer_path": layer_path,
         "options": {"wb_defer": a.wb_defer, "wb_stream": a.wb_stream, "spare_slots_per_layer": a.spare,
-                    "inclusive_blocks": inclusive},
+                    "inclusive_blocks": inclusive, "policy": a.policy, "round_every": a.round_every,
+                    "disk_queue": a.disk_queue},
     }
     if a.peer:
         # every expert lives in one rank's store: a miss is an NVLink pull from a peer or an HBM copy from the

@@ -16,7 +16,7 @@ class DgRun:
     def __init__(self, model, residents_per_layer=None, resident_keys=None, spare_per_layer=1, max_ids=2,
                  host_spare_units=None, diag=False, test_hooks=True, wb_defer=1, wb_stream=1, verify=False,
                  n_pred=0, slices=64, mode=0, timeout_ms=10000, device_bytes=None, with_reader=True,
-                 resident_order=None, inclusive=0, peer=None, disk_keys=(), disk_staging=0, disk_prefetch=0,
+                 resident_order=None, inclusive=0, peer=None, disk_keys=(), disk_staging=0, disk_prefetch=0, disk_queue=0,
                  policy=0, weights=None, profile=None):
         self.model = model
         G, U = model.layers, model.units
@@ -70,6 +70,7 @@ class DgRun:
             o.dg_disk_tier = 1
             o.dg_disk_staging = disk_staging
             o.dg_disk_prefetch = disk_prefetch
+            o.dg_disk_queue = disk_queue
         o.device = torch.cuda.current_device()  # the context lives on the engine's device
         self.ctx = runtime.DgContext(self.desc, self.plan, o, peer=peer)
         self.stream = torch.cuda.Stream()
