@@ -106,6 +106,16 @@ typedef struct tsb_dg_replay_config {
    * disk_overlapped, disk_max_in_flight, disk_carried, disk_carried_bytes */
   uint32_t disk_queue, reserved3;
   uint64_t* qstats;
+  /* kept-resident layers: after the boundary of token mr_token[i], event i holds gated layer mr_layer[i]'s units
+   * (mr_count[i] ids, the next ones of mr_ids) with ss_dg_make_resident, or releases it (mr_count[i] = 0); a held
+   * layer is not exported and its units are kept at every boundary and round. mstats (optional): [tokens][4]
+   * resident_units, resident_evicted, mkres_file_reads, mkres_wb_bytes */
+  uint32_t mr_n, reserved4;
+  const uint32_t* mr_token;
+  const uint32_t* mr_layer;
+  const uint32_t* mr_count;
+  const uint32_t* mr_ids;
+  uint64_t* mstats;
 } tsb_dg_replay_config;
 SS_API ss_status tsb_test_dg_replay(const tsb_dg_replay_config* cfg, const int32_t* ids, const int32_t* preds,
                                     int32_t* tables, uint64_t* stats, const uint8_t* src_units, uint64_t* read_sum);

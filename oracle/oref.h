@@ -51,6 +51,14 @@ typedef struct oref_dg_config {
    * disk_max_in_flight, disk_carried, disk_carried_bytes */
   uint32_t disk_queue, reserved3;
   uint64_t* qstats;
+  /* kept-resident layers: make_resident events after the boundary of mr_token[i] (mr_count[i] = 0: a release);
+   * mstats (optional): [tokens][4] resident_units, resident_evicted, mkres_file_reads, mkres_wb_bytes */
+  uint32_t mr_n, reserved4;
+  const uint32_t* mr_token;
+  const uint32_t* mr_layer;
+  const uint32_t* mr_count;
+  const uint32_t* mr_ids;
+  uint64_t* mstats;
 } oref_dg_config;
 #define OREF_NXSTATS 6
 

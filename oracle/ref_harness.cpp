@@ -185,9 +185,21 @@ extern "C" __attribute__((visibility("default"))) int oref_dg_replay(const oref_
       }
     std::vector<uint32_t> row(c->n_ids), pred(c->n_pred);
     uint64_t rsum[6] = {0, 0, 0, 0, 0, 0};
+      std::vector<std::vector<uint32_t>> held_keys(c->n_gated);  // kept-resident layers
+      std::vector<uint8_t> held(c->n_gated, 0);
+      auto kept_all = [&] {
+        std::vector<uint32_t> v;
+        for (const auto& h : held_keys) v.insert(v.end(), h.begin(), h.end());
+        return v;
+      };
     for (uint32_t tok = 0; tok < c->tokens; ++tok) {
-      core.begin_token(tok + 1);
+      std::vector<uint8_t> run(c->n_gated, 1);  // a held layer is not exported
+      for (uint32_t g = 0; g < c->n_gated; ++g) run[g] = held[g] ? 0 : 1;
+      core.begin_token(tok + 1, &run);
       for (uint32_t g = 0; g < c->n_gated; ++g) {
+        if (!run[g]) continue;
+        uint32_t nx = g + 1;
+        while (nx < c->n_gated && !run[nx]) ++nx;
         const int32_t* r = ids + (size_t(tok) * c->n_gated + g) * c->n_ids;
         uint64_t mask = 0;
         for (uint32_t i = 0; i < c->n_ids; ++i) {  // the export kernel's rule on the device table
@@ -201,23 +213,27 @@ extern "C" __attribute__((visibility("default"))) int oref_dg_replay(const oref_
             read_sum[(size_t(tok) * c->n_gated + g) * c->n_ids + i] = s < 0 ? 0 : checksum(t.slot_ptr(s), t.unit_);
           }
         core.serve_use(g, row.data(), c->n_ids, mask);
-        if (preds && c->n_pred && g + 1 < c->n_gated) {
+        if (preds && c->n_pred && g + 1 < c->n_gated && run[g + 1]) {
           const int32_t* p = preds + (size_t(tok) * c->n_gated + g) * c->n_pred;
           for (uint32_t i = 0; i < c->n_pred; ++i) pred[i] = uint32_t(p[i]);
           core.serve_prediction(g + 1, pred.data(), c->n_pred, c->n_ids, false);
         }
-        if (core.deferred() && g + 1 < c->n_gated) core.issue_writebacks(g, [] { return false; });
+        if (core.deferred() && nx < c->n_gated) core.issue_writebacks(g, [] { return false; });
         if (core.scored()) core.score_layer(g);  // (the service closes each layer after its work, scored only)
       }
-      core.end_token({}, c->rows ? c->rows : 1);
-      if (c->reset_at && tok + 1 == c->reset_at) core.reset_open();
+      core.end_token(kept_all(), c->rows ? c->rows : 1);
+      if (c->reset_at && tok + 1 == c->reset_at) {  // every keep and hold dropped
+        core.reset_open();
+        for (auto& h : held_keys) h.clear();
+        std::fill(held.begin(), held.end(), uint8_t(0));
+      }
       if (c->round_every && (tok + 1) % c->round_every == 0) {  // ss_dg_round between tokens, nothing kept
         ts::DgRoundIn in;
         in.budget_bytes = c->round_budget;
         in.max_units = c->round_max_units;
         in.hysteresis = double(c->round_hysteresis);
         in.decay = double(c->round_decay);
-        const ts::DgRoundOut r = core.round(in, {});
+        const ts::DgRoundOut r = core.round(in, kept_all());
         rsum[0] += 1;
         rsum[1] += r.promoted_to_device;
         rsum[2] += r.promoted_to_pinned;
@@ -225,7 +241,26 @@ extern "C" __attribute__((visibility("default"))) int oref_dg_replay(const oref_
         rsum[4] += r.dropped_to_file;
         rsum[5] += r.bytes_read + r.bytes_h2d + r.bytes_written_back;
       }
+      for (uint32_t i = 0, at = 0; i < c->mr_n; at += c->mr_count[i], ++i) {  // kept-resident events
+        if (c->mr_token[i] != tok) continue;
+        const uint32_t lg = c->mr_layer[i];
+        std::vector<uint32_t> want(c->mr_ids + at, c->mr_ids + at + c->mr_count[i]), held_now;
+        if (want.empty()) {
+          held_keys[lg].clear();
+          held[lg] = 0;
+          continue;
+        }
+        core.make_resident(lg, want, kept_all());
+        for (uint32_t u : want) held_now.push_back(core.key(lg, u));
+        held_keys[lg] = held_now;
+        held[lg] = 1;
+      }
       if (c->rstats) std::memcpy(c->rstats + size_t(tok) * 6, rsum, sizeof rsum);
+      if (c->mstats) {
+        const auto& q = core.stats();
+        const uint64_t mv[4] = {q.resident_units, q.resident_evicted, q.mkres_file_reads, q.mkres_wb_bytes};
+        std::memcpy(c->mstats + size_t(tok) * 4, mv, sizeof mv);
+      }
       if (c->qstats) {
         const ts::DgStats& q = core.stats();
         const uint64_t qv[4] = {q.disk_overlapped, q.disk_max_in_flight, q.disk_carried, q.disk_carried_bytes};

@@ -147,7 +147,9 @@ class dg_replay_config(C.Structure):
                 ("round_hysteresis", C.c_float), ("round_decay", C.c_float), ("round_budget", u64),
                 ("rstats", C.POINTER(u64)), ("no_admit", u32), ("clean_evict", u32), ("pf_revert", u32),
                 ("pf_strict", u32), ("pstats", C.POINTER(u64)), ("disk_queue", u32), ("reserved3", u32),
-                ("qstats", C.POINTER(u64))]
+                ("qstats", C.POINTER(u64)), ("mr_n", u32), ("reserved4", u32), ("mr_token", C.POINTER(u32)),
+                ("mr_layer", C.POINTER(u32)), ("mr_count", C.POINTER(u32)), ("mr_ids", C.POINTER(u32)),
+                ("mstats", C.POINTER(u64))]
 
 
 class ss_dg_round_params(C.Structure):

@@ -251,17 +251,20 @@ void SlotCache::to_lower(uint32_t k, bool cold) {
   }
 }
 
-// The least recently homed pinned unit goes to its file (no copy: the file holds its bytes); its block is free.
-bool SlotCache::drop_host_lru() {
-  if (!c_.disk_tier || htail_ == kNil) return false;
-  const uint32_t k = htail_;
+// The least recently homed pinned unit (not skipped) goes to its file (no copy: the file holds its bytes); its block
+// is free.
+bool SlotCache::drop_host_lru(const std::vector<uint8_t>* skip, bool count) {
+  if (!c_.disk_tier) return false;
+  uint32_t k = htail_;
+  while (k != kNil && skip && (*skip)[k]) k = e_[k].hprev;
+  if (k == kNil) return false;
   Entry& x = e_[k];
   hunlink(k);
   free_blocks_.push_back(x.block);
   x.block = -1;
   x.home = Home::File;
   ++on_file_;
-  ++st_.disk_drops;
+  if (count) ++st_.disk_drops;
   return true;
 }
 
@@ -1120,15 +1123,15 @@ SlotCache::ScoreCand SlotCache::score_candidate(uint32_t g, uint32_t u, uint64_t
 
 // The `need` lowest candidates (cand_less) of every gated layer's eligible units, ascending in select_heap_: a bounded
 // max-heap over all layers, scored from each layer's current union, epochs and stamps.
-void SlotCache::select_scored(size_t need, const std::function<bool(uint32_t)>& eligible) {
+void SlotCache::select_scored(size_t need, const std::function<bool(uint32_t)>& eligible, bool count) {
   select_heap_.clear();
   for (uint32_t g = 0; need && g < gated(); ++g) {
     uint64_t D = 0;
     for (uint32_t r : sc_[g].cur) D += sc_[g].rowsum[r];
-    ++st_.score_layers;
+    if (count) ++st_.score_layers;
     for (uint32_t u = 0; u < units(g); ++u) {
       if (!eligible(base_[g] + u)) continue;
-      ++st_.score_candidates;
+      if (count) ++st_.score_candidates;
       const ScoreCand cd = score_candidate(g, u, D, select_heap_.size() == need ? &select_heap_.front() : nullptr);
       if (select_heap_.size() < need) {
         select_heap_.push_back(cd);
@@ -1196,6 +1199,307 @@ void SlotCache::load_counts(const std::vector<std::vector<uint32_t>>& cells) {
     }
     l.open_T = l.T;  // the reset_open state
   }
+}
+
+// ---- kept-resident layers (ss_dg_make_resident) ----
+SlotCache::ResidentResult SlotCache::make_resident(uint32_t g, const std::vector<uint32_t>& ids,
+                                                   const std::vector<uint32_t>& other_kept) {
+  const auto t0 = std::chrono::steady_clock::now();
+  require(g < gated(), SS_E_INVALID, "ss_dg_make_resident: gated layer out of range");
+  std::vector<uint8_t> want(keys_, 0), other(keys_, 0);
+  for (uint32_t u : ids) {
+    require(u < units(g), SS_E_INVALID, "ss_dg_make_resident: id out of range");
+    require(!want[key(g, u)], SS_E_INVALID, "ss_dg_make_resident: duplicate id " + std::to_string(u));
+    want[key(g, u)] = 1;
+  }
+  size_t n_other = 0;
+  for (uint32_t k : other_kept)
+    if (k < keys_ && !other[k] && !want[k]) {
+      other[k] = 1;
+      ++n_other;
+    }
+  // capacity: every layer's kept units leave the spare target free for the boundaries
+  const uint64_t cap = uint64_t(c_.persistent_slots) - c_.spare_target;
+  require(ids.size() + n_other <= cap, SS_E_CAPACITY,
+          "ss_dg_make_resident: " + std::to_string(ids.size()) + " units of gated layer " + std::to_string(g) + " + " +
+              std::to_string(n_other) + " other kept units + the spare target " + std::to_string(c_.spare_target) +
+              " exceed the " + std::to_string(c_.persistent_slots) + " persistent slots");
+  size_t need = 0, eligible_n = 0, evicting = 0, discarded = 0;
+  for (uint32_t k = 0; k < keys_; ++k) {
+    const Entry& x = e_[k];
+    require(x.home != Home::Bank, SS_E_BACKEND, "ss_dg_make_resident: a bank unit between tokens");
+    if (x.home == Home::Evicting) ++evicting;
+    if (want[k]) need += x.home != Home::Device && x.home != Home::Coming ? 1u : 0u;
+    else if (x.home == Home::Device && !other[k]) ++eligible_n;
+  }
+  for (const Writeback& w : wbs_) discarded += w.discard ? 1u : 0u;
+  const size_t free_after = free_slots_.size() + evicting;
+  require(need <= free_after + eligible_n, SS_E_CAPACITY,
+          "ss_dg_make_resident: " + std::to_string(need) + " units to copy in, " + std::to_string(free_after) +
+              " free slots and " + std::to_string(eligible_n) +
+              " evictable units (the rest hold other layers' kept units or prefetches in flight)");
+  require(c_.disk_tier || need <= free_after || free_after + free_blocks_.size() + discarded > 0, SS_E_CAPACITY,
+          "ss_dg_make_resident: no free slot and no free pinned block to start the write-backs");
+  stamp_room("ss_dg_make_resident");
+  drain();  // everything settled: reads, copies, deferred and recorded write-backs collected
+  for (const Writeback& w : wbs_) m_->event_sync(w.done);
+  collect();
+  if (!wbs_.empty()) broken("ss_dg_make_resident: write-backs not collected");
+
+  ResidentResult r;
+  std::vector<uint32_t> in;  // the units to copy in, in the caller's order
+  for (uint32_t u : ids) {
+    const uint32_t k = key(g, u);
+    Entry& x = e_[k];
+    if (x.home == Home::Coming) {  // a prefetch whose copy landed: admitted now
+      x.home = Home::Device;
+      x.via_pf = false;
+      if (x.pf_done) {
+        pool_.push_back(x.pf_done);
+        x.pf_done = nullptr;
+      }
+      if (x.block >= 0) {
+        free_blocks_.push_back(x.block);
+        x.block = -1;
+      }
+    } else if (x.home != Home::Device) {
+      in.push_back(k);
+    }
+  }
+  auto eligible = [&](uint32_t k) {
+    const Entry& x = e_[k];
+    return x.home == Home::Device && !x.wb_pending && !want[k] && !other[k];
+  };
+  std::vector<uint32_t> victims;
+  const size_t n_vict = in.size() > free_slots_.size() ? in.size() - free_slots_.size() : 0;
+  if (n_vict && c_.scored) {
+    select_scored(n_vict, eligible, false);
+    for (const ScoreCand& cd : select_heap_) victims.push_back(cd.key);
+  } else {
+    for (uint32_t k = tail_; k != kNil && victims.size() < n_vict; k = e_[k].prev)
+      if (eligible(k)) victims.push_back(k);
+  }
+  if (victims.size() != n_vict) broken("ss_dg_make_resident: fewer victims than the capacity check counted");
+
+  std::vector<uint8_t> hold = want;  // never dropped to a file here: the units to copy in, this call's write-backs
+  std::vector<int32_t> released;     // source blocks of committed copies (free once the demand stream synced)
+  std::vector<int32_t> wb;           // slots of written-back victims (free once the write-back stream synced)
+  struct Read {
+    uint32_t key;
+    int32_t slot, stage;
+    void* handle;
+  };
+  std::deque<Read> reads;  // file reads in flight, oldest first, each in its own staging buffer
+  const size_t depth = c_.disk_tier ? std::max<size_t>(1, std::min<size_t>(std::max<uint32_t>(c_.disk_queue, 1),
+                                                                          c_.disk_staging))
+                                    : 1;
+  bool io_error = false;
+  // the committed units become the most recent in the order of `in` on every exit
+  struct Recent {
+    SlotCache* cache;
+    const std::vector<uint32_t>& order;
+    std::vector<uint8_t> done;
+    ~Recent() {
+      for (size_t i = 0; i < order.size(); ++i)
+        if (done[i]) cache->push_front(order[i]);
+    }
+  } recent{this, in, std::vector<uint8_t>(in.size(), 0)};
+  std::vector<int32_t> in_pos(keys_, -1);
+  for (size_t i = 0; i < in.size(); ++i) in_pos[in[i]] = int32_t(i);
+  auto commit = [&](uint32_t k, int32_t slot) {
+    Entry& x = e_[k];
+    x.home = Home::Device;
+    x.slot = slot;
+    x.block = -1;
+    recent.done[size_t(in_pos[k])] = 1;
+    ++on_device_;
+    ++r.copied;
+  };
+  auto transfer = [&](uint32_t k, int32_t slot, int32_t src) {  // the copy and its entry, or nothing owned changes
+    try {
+      m_->h2d(Mover::kDem, slot, src, k);
+      publish(Mover::kDem, k, slot);
+    } catch (...) {
+      table_[k] = -1;
+      free_slots_.push_back(slot);
+      throw;
+    }
+  };
+  auto flush_dem = [&] {
+    m_->sync(Mover::kDem);
+    free_blocks_.insert(free_blocks_.end(), released.begin(), released.end());
+    released.clear();
+  };
+  auto flush_d2h = [&] {
+    if (wb.empty()) return;
+    m_->sync(Mover::kD2h);
+    free_slots_.insert(free_slots_.end(), wb.begin(), wb.end());
+    wb.clear();
+  };
+  uint64_t n_read = 0, n_wb = 0, read_ns = 0;
+  auto timed = [&](const std::chrono::steady_clock::time_point& a) {
+    read_ns += uint64_t(
+        std::chrono::duration_cast<std::chrono::nanoseconds>(std::chrono::steady_clock::now() - a).count());
+  };
+  auto end_read = [&](size_t i) {  // a read's end: its copy and entry, its staging buffer's event
+    const Read rd = reads[i];
+    reads.erase(reads.begin() + std::ptrdiff_t(i));
+    const auto ta = std::chrono::steady_clock::now();
+    try {
+      m_->read_end(rd.handle);
+    } catch (...) {
+      timed(ta);
+      io_error = true;
+      free_slots_.push_back(rd.slot);
+      throw;
+    }
+    timed(ta);
+    transfer(rd.key, rd.slot, rd.stage);
+    --on_file_;
+    commit(rd.key, rd.slot);
+    ++n_read;
+    void*& ev = stage_ev_[uint32_t(rd.stage) - c_.blocks];
+    if (!ev) ev = event();
+    m_->record(ev, Mover::kDem);
+  };
+  auto account = [&] {
+    st_.resident_units += r.copied;
+    st_.resident_evicted += r.evicted;
+    st_.resident_bytes += uint64_t(r.copied) * unit_bytes_;
+    st_.mkres_file_reads += n_read;
+    st_.mkres_file_bytes += n_read * unit_bytes_;
+    st_.mkres_read_ns += read_ns;
+    st_.mkres_h2d_bytes += uint64_t(r.copied) * unit_bytes_;
+    st_.mkres_wb_bytes += n_wb * unit_bytes_;
+    st_.resident_ns += uint64_t(
+        std::chrono::duration_cast<std::chrono::nanoseconds>(std::chrono::steady_clock::now() - t0).count());
+  };
+  try {
+    size_t next = 0, vi = 0;
+    while (next < in.size()) {
+      // no free slot: the next victims (as many as the remaining units need and the blocks allow)
+      const bool evict = free_slots_.empty();
+      while (evict && vi < victims.size() && free_slots_.size() + wb.size() < in.size() - next) {
+        const uint32_t v = victims[vi];
+        Entry& x = e_[v];
+        if (!x.backed && free_blocks_.empty() && !released.empty()) {  // the blocks of the copies already enqueued
+          flush_dem();
+          continue;
+        }
+        if (!x.backed && free_blocks_.empty() && !c_.disk_tier) break;
+        // a clean copy (its block is its home again) or, file tier with no block to free (clean_evict: none
+        // free), its file: no copy
+        const bool clean = !x.backed && clean_now();
+        const bool no_copy = x.backed || clean || (free_blocks_.empty() && !drop_host_lru(&hold, false));
+        if (clean) count_clean();
+        int32_t b = -1;
+        if (!no_copy) {
+          b = free_blocks_.back();
+          m_->d2h(Mover::kD2h, x.slot, b, -1, v);  // the dirty unit's only copy, written back before its slot is reused
+          free_blocks_.pop_back();
+          ++n_wb;
+        }
+        ++vi;
+        ++r.evicted;
+        unlink(v);
+        --on_device_;
+        table_[v] = -1;
+        if (no_copy) {
+          free_slots_.push_back(x.slot);
+          to_lower(v);
+          continue;
+        }
+        wb.push_back(x.slot);
+        x.home = Home::Host;
+        x.slot = -1;
+        x.block = b;
+        hpush(v);
+        hold[v] = 1;
+      }
+      flush_d2h();
+      if (free_slots_.empty()) fail(SS_E_BACKEND, "ss_dg_make_resident: no slot for a unit");
+      const int32_t slot = free_slots_.back();
+      free_slots_.pop_back();
+      const uint32_t k = in[next];
+      Entry& x = e_[k];
+      if (x.home == Home::Host) {
+        const int32_t b = x.block;
+        transfer(k, slot, b);
+        ++next;
+        hunlink(k);
+        released.push_back(b);
+        commit(k, slot);
+        continue;
+      }
+      // its file, through the next staging buffer (its last copy landed first): at most `depth` reads in flight, the
+      // finished ones ending first (any position), then the oldest; a read holding the next buffer ends before it
+      try {
+        if (reads.size() >= depth)
+          for (size_t j = 0; j < reads.size();) {
+            if (m_->read_done(reads[j].handle)) end_read(j);
+            else ++j;
+          }
+        if (reads.size() >= depth) end_read(0);
+        const uint32_t i = stage_next_;
+        stage_next_ = (i + 1) % c_.disk_staging;
+        const int32_t stage = int32_t(c_.blocks + i);
+        for (size_t j = 0; j < reads.size(); ++j)
+          if (reads[j].stage == stage) {
+            end_read(j);
+            break;
+          }
+        if (stage_ev_[i] && !m_->done(stage_ev_[i])) m_->event_sync(stage_ev_[i]);
+        void* h = nullptr;
+        const auto tb = std::chrono::steady_clock::now();
+        try {
+          h = m_->read_begin(k, stage);
+        } catch (...) {
+          timed(tb);
+          io_error = true;
+          throw;
+        }
+        timed(tb);
+        reads.push_back({k, slot, stage, h});
+        ++next;
+      } catch (...) {
+        free_slots_.push_back(slot);
+        throw;
+      }
+    }
+    while (!reads.empty()) end_read(0);
+    flush_d2h();
+    flush_dem();
+    m_->upload_table(table_.data(), keys_);  // (syncs the demand stream) every changed entry, the victims' -1 included
+  } catch (...) {
+    for (const Read& rd : reads) {  // reads not ended give their slots back (their keys never changed home)
+      try {
+        m_->read_end(rd.handle);
+      } catch (...) {
+      }
+      free_slots_.push_back(rd.slot);
+    }
+    reads.clear();
+    bool ok = false;
+    if (io_error) {  // the device is fine: what was enqueued lands, the table goes up
+      try {
+        flush_d2h();
+        flush_dem();
+        m_->upload_table(table_.data(), keys_);
+        ok = true;
+      } catch (...) {
+      }
+    }
+    if (!ok) {  // a device failure: the host records stay one ownership (the context is poisoned by its caller)
+      free_slots_.insert(free_slots_.end(), wb.begin(), wb.end());
+      wb.clear();
+      free_blocks_.insert(free_blocks_.end(), released.begin(), released.end());
+      released.clear();
+    }
+    account();
+    throw;
+  }
+  account();
+  return r;
 }
 
 // ---- placement rounds ----

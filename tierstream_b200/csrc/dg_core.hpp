@@ -158,6 +158,10 @@ struct CacheStats {
   // opt-in policies: victims dropped to their file by clean_evict and their bytes; unused prefetches reverted and
   // their bytes; prefetches pf_strict refused
   uint64_t clean_drops = 0, clean_drop_bytes = 0, pf_reverted = 0, pf_revert_bytes = 0, pf_strict_refused = 0;
+  // make_resident: units copied in and evicted, bytes copied in, host time; its file reads, their bytes and time,
+  // its write-back bytes
+  uint64_t resident_units = 0, resident_evicted = 0, resident_bytes = 0, resident_ns = 0;
+  uint64_t mkres_file_reads = 0, mkres_file_bytes = 0, mkres_read_ns = 0, mkres_h2d_bytes = 0, mkres_wb_bytes = 0;
 };
 
 // A placement round's limits and what it did (ss_dg_round_params / ss_dg_round_result without the struct sizes).
@@ -245,6 +249,15 @@ class SlotCache {
   // A score profile's transition counts (units(g)^2 per gated layer, row-major [previous unit][unit]) as the open
   // state of the tables (scored only; kept for reset_open).
   void load_counts(const std::vector<std::vector<uint32_t>>& cells);
+  // Between tokens: gated layer g's units `units` (distinct ids) all on the device (ss_dg_make_resident), the call's
+  // other protected keys `other_kept` never evicted. Every refusal comes before any action; then every copy landed
+  // and the table is uploaded when it returns. Victims in the policy's order (the recency tail, or scores) with the
+  // boundary's lower-tier rules; copies in from the pinned block or, through the staging buffers, the file; the units
+  // copied in become the most recent (dg_core.cpp:2248-2590).
+  struct ResidentResult {
+    uint32_t copied = 0, evicted = 0;
+  };
+  ResidentResult make_resident(uint32_t g, const std::vector<uint32_t>& units, const std::vector<uint32_t>& other_kept);
   // Between tokens: one placement round (kept: keys that never move). Every copy landed and the table is uploaded when
   // it returns.
   RoundOut round(const RoundIn& in, const std::vector<uint32_t>& kept);
@@ -342,7 +355,7 @@ class SlotCache {
   }
   void score_history(uint32_t g);
   ScoreCand score_candidate(uint32_t g, uint32_t u, uint64_t denominator, const ScoreCand* cutoff) const;
-  void select_scored(size_t need, const std::function<bool(uint32_t)>& eligible);
+  void select_scored(size_t need, const std::function<bool(uint32_t)>& eligible, bool count = true);
   void reset_score();
   void stamp_room(const char* what) const;
   void* event();
@@ -361,7 +374,8 @@ class SlotCache {
     st_.clean_drop_bytes += unit_bytes_;
   }
   void hunlink(uint32_t k);
-  bool drop_host_lru();
+  // the least recently homed pinned unit not in `skip` to its file; count: a disk drop of the boundary
+  bool drop_host_lru(const std::vector<uint8_t>* skip = nullptr, bool count = true);
   int32_t take_stage();
   void publish(Mover::Stream s, uint32_t k, int32_t v);
   bool fetch(uint32_t g, uint32_t unit, bool prefetch);

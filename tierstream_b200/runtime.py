@@ -258,7 +258,7 @@ def replay_config(n_units, part_bytes, persistent_slots, bank_slots, blocks, spa
                   wb_on_d2h=1, wb_layer_bytes=0, wb_max_outstanding=0, move_bytes=0, inclusive=0, disk=None,
                   home_blocks=0, disk_staging=0, disk_prefetch=0, policy=0, rows=1, weights=None, profile=None,
                   round_every=0, round_max_units=96, round_hysteresis=1.25, round_decay=0.85, round_budget=0,
-                  no_admit=0, clean_evict=0, pf_revert=0, pf_strict=0, disk_queue=0):
+                  no_admit=0, clean_evict=0, pf_revert=0, pf_strict=0, disk_queue=0, resident_events=()):
     """A dg_replay_config with its arrays kept alive on the returned object. disk (file tier): one flag per key for
     the plan's disk units (blocks then counts home_blocks + the spare blocks); xstats is attached by replay().
     policy (scored eviction): 0 LRU, 1 SCORED, 2 SCORED_AUTO, with each boundary's row count `rows`, weights
@@ -283,6 +283,16 @@ def replay_config(n_units, part_bytes, persistent_slots, bank_slots, blocks, spa
     c.policy, c.rows = policy, rows
     c.no_admit, c.clean_evict, c.pf_revert, c.pf_strict = no_admit, clean_evict, pf_revert, pf_strict
     c.disk_queue = disk_queue
+    if resident_events:  # (token, gated layer, ids): ss_dg_make_resident after that token's boundary; ids () = release
+        ev = list(resident_events)
+        keep["mr_token"] = (C.c_uint32 * len(ev))(*[e[0] for e in ev])
+        keep["mr_layer"] = (C.c_uint32 * len(ev))(*[e[1] for e in ev])
+        keep["mr_count"] = (C.c_uint32 * len(ev))(*[len(e[2]) for e in ev])
+        flat = [u for e in ev for u in e[2]]
+        keep["mr_ids"] = (C.c_uint32 * max(1, len(flat)))(*flat)
+        c.mr_n = len(ev)
+        c.mr_token, c.mr_layer, c.mr_count, c.mr_ids = (keep["mr_token"], keep["mr_layer"], keep["mr_count"],
+                                                          keep["mr_ids"])
     c.round_every, c.round_max_units, c.round_hysteresis, c.round_decay, c.round_budget = \
         round_every, round_max_units, round_hysteresis, round_decay, round_budget
     if weights:
@@ -300,7 +310,7 @@ def replay_config(n_units, part_bytes, persistent_slots, bank_slots, blocks, spa
 
 
 def replay(cfg, ids, preds=None, src_units=None, want_reads=False, xstats=None, rstats=None, pstats=None,
-           qstats=None):
+           qstats=None, mstats=None):
     """This library's deterministic replay (tsb_test_dg_replay): (tables, stats[, read_sum]). xstats: an optional
     uint64 array [tokens][6] filled with the file tier's counters after each boundary."""
     keys = sum(cfg.n_units[i] for i in range(cfg.n_gated))
@@ -308,6 +318,7 @@ def replay(cfg, ids, preds=None, src_units=None, want_reads=False, xstats=None, 
     cfg.rstats = rstats.ctypes.data_as(C.POINTER(C.c_uint64)) if rstats is not None else None  # [tokens][6] rounds
     cfg.pstats = pstats.ctypes.data_as(C.POINTER(C.c_uint64)) if pstats is not None else None  # [tokens][5]
     cfg.qstats = qstats.ctypes.data_as(C.POINTER(C.c_uint64)) if qstats is not None else None  # [tokens][4]
+    cfg.mstats = mstats.ctypes.data_as(C.POINTER(C.c_uint64)) if mstats is not None else None  # [tokens][4]
     ids = np.ascontiguousarray(ids, dtype=np.int32)
     tables = np.empty((cfg.tokens, keys), dtype=np.int32)
     stats = np.empty((cfg.tokens, 16), dtype=np.uint64)
