@@ -907,7 +907,9 @@ int ss_budget_ledger_within_caps(const ss_budget_ledger*) { return 0; }
 ss_status ss_budget_in_dg_library(ss_budget_in*, const ss_desc*, const ss_options*) {
   return unsupported("ss_budget_in_dg_library");
 }
-ss_status ss_dg_make_resident(ss_ctx*, int, const int32_t*, int) { return unsupported("ss_dg_make_resident"); }
+ss_status ss_dg_make_resident(ss_ctx* c, int g, const int32_t* ids, int n) {
+  return ctx_guard(c, [&] { dg_of(c, "ss_dg_make_resident").make_resident(g, ids, n); });
+}
 namespace {
 void round_defaults(ss_dg_round_params* p) {
   *p = ss_dg_round_params{};

@@ -61,6 +61,7 @@ class DgContext {
   virtual void enqueue_wait(int g, void* s) = 0;
   virtual void enqueue_end(void* s) = 0;
   virtual void keep(int g, const int32_t* ids, int n) = 0;
+  virtual void make_resident(int g, const int32_t* ids, int n) = 0;
   virtual uint32_t residency(ss_dg_unit* out, uint32_t cap) = 0;
   virtual void set_sched(uint32_t wb_defer, uint32_t flush_ready) = 0;
   virtual void set_budgets(uint32_t spare_target, uint32_t per_layer, uint32_t per_token) = 0;

@@ -859,7 +859,8 @@ class CudaDgContext final : public DgContext {
     require(!in_token_, SS_E_INVALID, "ss_begin: a gated token is already open (call ss_end)");
     if (rows) require(n_layers == int(d_.layers.size()), SS_E_INVALID, "ss_begin: rows_per_layer must cover every layer");
     const uint32_t G = uint32_t(x_.gated.size());
-    for (uint32_t g = 0; g < G; ++g) run_[g] = rows ? uint8_t(rows[x_.gated[g]] != 0) : uint8_t(1);
+    for (uint32_t g = 0; g < G; ++g)  // (a held layer is not exported)
+      run_[g] = uint8_t((rows ? rows[x_.gated[g]] != 0 : true) && !held_[g]);
     // no step ran outside a pair: every word still holds the last token's sequence
     bool clean = load_acquire(m_.done) == seq_ && load_acquire(m_.began) == seq_;
     for (uint32_t g = 0; clean && g < G; ++g)
@@ -1029,6 +1030,29 @@ class CudaDgContext final : public DgContext {
       keys.push_back(core_->key(uint32_t(g), uint32_t(ids[i])));
     }
     keep_[size_t(g)] = std::move(keys);
+    held_[size_t(g)] = 0;  // a plain keep: g is exported again
+  }
+  // ss_dg_make_resident: the units of gated layer g all on the device and kept there; g is not exported while held (the
+  // engine reads its units through the table without an export); n = 0 releases it.
+  void make_resident(int g, const int32_t* ids, int n) override {
+    require(!in_token_, SS_E_INVALID, "ss_dg_make_resident: between tokens only");
+    check_g(g, "ss_dg_make_resident");
+    require(n >= 0 && (n == 0 || ids), SS_E_INVALID, "ss_dg_make_resident: bad arguments");
+    if (n == 0) {
+      keep_[size_t(g)].clear();
+      held_[size_t(g)] = 0;
+      return;
+    }
+    std::vector<uint32_t> units, keys;
+    for (int i = 0; i < n; ++i) {
+      require(ids[i] >= 0 && uint32_t(ids[i]) < core_->units(uint32_t(g)), SS_E_INVALID,
+              "ss_dg_make_resident: id out of range");
+      units.push_back(uint32_t(ids[i]));
+      keys.push_back(core_->key(uint32_t(g), uint32_t(ids[i])));
+    }
+    core_->make_resident(uint32_t(g), units, keep_all());  // a refusal changes nothing (g keeps its former keep)
+    keep_[size_t(g)] = std::move(keys);
+    held_[size_t(g)] = 1;
   }
   uint32_t residency(ss_dg_unit* out, uint32_t cap) override {
     require(!in_token_, SS_E_INVALID, "ss_dg_residency: between tokens only");
@@ -1167,6 +1191,15 @@ class CudaDgContext final : public DgContext {
     s.round_bytes = d(c.round_bytes, base_.round_bytes);
     s.round_ns = d(c.round_ns, base_.round_ns);
     s.round_cancelled = d(c.round_cancelled, base_.round_cancelled);
+    s.resident_units = d(c.resident_units, base_.resident_units);
+    s.resident_evicted = d(c.resident_evicted, base_.resident_evicted);
+    s.resident_bytes = d(c.resident_bytes, base_.resident_bytes);
+    s.resident_ns = d(c.resident_ns, base_.resident_ns);
+    s.mkres_file_reads = d(c.mkres_file_reads, base_.mkres_file_reads);
+    s.mkres_file_bytes = d(c.mkres_file_bytes, base_.mkres_file_bytes);
+    s.mkres_read_ns = d(c.mkres_read_ns, base_.mkres_read_ns);
+    s.mkres_h2d_bytes = d(c.mkres_h2d_bytes, base_.mkres_h2d_bytes);
+    s.mkres_wb_bytes = d(c.mkres_wb_bytes, base_.mkres_wb_bytes);
     s.clean_drops = d(c.clean_drops, base_.clean_drops);
     s.clean_drop_bytes = d(c.clean_drop_bytes, base_.clean_drop_bytes);
     s.pf_reverted = d(c.pf_reverted, base_.pf_reverted);
@@ -1257,6 +1290,7 @@ class CudaDgContext final : public DgContext {
     try {
       core_->reset_open();
       for (auto& k : keep_) k.clear();
+      std::fill(held_.begin(), held_.end(), uint8_t(0));
     } catch (...) {
       poisoned_ = true;
       throw;
@@ -1605,6 +1639,7 @@ class CudaDgContext final : public DgContext {
     mover_->upload_table(core_->table().data(), x_.keys);
     core_->check();
     keep_.assign(G, {});
+    held_.assign(G, 0);
     run_.assign(G, 1);
     lbase_.assign(G, LayerCounts{});
     svc_ = std::make_unique<Service>(core_.get(), m_, x_.B, o_.dg_wait_timeout_ms, device_, mover_->deterministic(),
@@ -1796,6 +1831,7 @@ class CudaDgContext final : public DgContext {
   std::unique_ptr<CudaMover> mover_;
   std::unique_ptr<SlotCache> core_;
   std::unique_ptr<Service> svc_;
+  std::vector<uint8_t> held_;  // gated layers holding a ss_dg_make_resident set (not exported)
   std::vector<std::vector<uint32_t>> keep_;
   std::vector<uint8_t> run_;
   uint32_t seq_ = 0;
