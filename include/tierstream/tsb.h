@@ -153,6 +153,14 @@ SS_API ss_status tsb_test_resident_replay(int32_t n_units, int32_t capacity, int
                                          const int32_t* max_ev, const uint8_t* admit_misses, int32_t* slots_out,
                                          int32_t* counts_out);
 
+/* Test hook: the device-gated layout ss_open would take for d, p and o (no device work, SS_E_* as ss_open refuses):
+ * out[n_out] = keys, R (residents), D (spare slots), B (bank size), P (pinned units), Q (spare blocks), I (inclusive
+ * share), F (file units), S (staging buffers), disk_queue, blocks, persistent_slots, slots, guard_slot, unit_bytes,
+ * host_stride, disk_tier, disk_prefetch, scored, w_trans, w_freq, w_rec, the resident count (at most 23 values);
+ * residents[cap]: the residents' keys. */
+SS_API ss_status tsb_test_dg_layout(const ss_desc* d, const ss_plan* p, const ss_options* o, uint64_t* out,
+                                    uint32_t n_out, uint32_t* residents, uint32_t cap);
+
 /* Test hooks of scored eviction's profile (the reference's TSSCPRF1 format, ss.h "Scored eviction"): the SHA-256 of
  * len bytes into out[32]; the profile identity of d's gated layers (every layer with units) into identity[32] and,
  * when profile is given, every rule of the format checked (SS_E_INVALID naming the first one broken) and its counts

@@ -19,6 +19,9 @@
 
 #include "backend.hpp"
 #include "desc.hpp"
+#include "errors.hpp"
+#include "json.hpp"
+#include "dg_layout.hpp"
 #include "dg_ctx.hpp"
 #include "plan.hpp"
 #include "resident_set.hpp"
@@ -182,6 +185,33 @@ extern "C" __attribute__((visibility("default"))) int oref_resident_replay(
       c[4] = a.deferred;
     }
     return 0;
+  } catch (const std::exception& e) {
+    if (err && errlen) std::snprintf(err, errlen, "%s", e.what());
+    return -1;
+  }
+}
+
+// The reference's own device-gated layout (dg_layout.cpp) of a descriptor, tiers, budget and options: the same numbers
+// as this library's layout hook, or its refusal (status and message).
+extern "C" __attribute__((visibility("default"))) int oref_dg_layout(const char* desc_json, size_t len,
+                                                                      const uint8_t* tiers, size_t n_tiers,
+                                                                      const ss_budget* budget, const ss_options* opt,
+                                                                      uint64_t* out, uint32_t n_out,
+                                                                      uint32_t* residents, uint32_t cap, char* err,
+                                                                      size_t errlen) {
+  try {
+    const ts::Desc d = ts::desc_from_json(ts::json_parse(std::string(desc_json, len)));
+    const ts::Plan p = ts::plan_from_tiers(d, *budget, std::vector<uint8_t>(tiers, tiers + n_tiers));
+    const ts::DgLayout x = ts::dg_layout(d, p, *opt);
+    const uint64_t v[23] = {x.keys, x.R, x.D, x.B, x.P, x.Q, x.I, x.F, x.S, x.disk_queue, x.blocks,
+                            x.persistent_slots, x.slots, x.guard_slot, x.unit_bytes, x.host_stride, x.disk_tier,
+                            x.disk_prefetch, x.scored, x.w_trans, x.w_freq, x.w_rec, x.residents.size()};
+    for (uint32_t i = 0; i < n_out && i < 23; ++i) out[i] = v[i];
+    for (uint32_t i = 0; i < cap && i < x.residents.size(); ++i) residents[i] = x.residents[i];
+    return 0;
+  } catch (const ts::Error& e) {
+    if (err && errlen) std::snprintf(err, errlen, "%s", e.what());
+    return int(e.status());
   } catch (const std::exception& e) {
     if (err && errlen) std::snprintf(err, errlen, "%s", e.what());
     return -1;

@@ -245,6 +245,7 @@ _PROTOS = {
     "tsb_move_timeouts": (C.c_int, []),
     "tsb_test_file_read": (C.c_int, [C.c_char_p, u64, u64, vp, u64, u32, C.c_int]),
     "tsb_test_sha256": (C.c_int, [vp, u64, vp]),
+    "tsb_test_dg_layout": (C.c_int, [vp, vp, P(ss_options), P(u64), u32, vp, u32]),
     "tsb_test_async_reads": (C.c_int, [C.c_char_p, P(u64), u32, u64, vp, u32, C.c_int]),
     "tsb_test_resident_replay": (C.c_int, [C.c_int32, C.c_int32, C.c_int32, u32, vp, vp, u32, u32, vp, u32, vp, vp,
                                            vp, vp, vp]),

@@ -711,6 +711,18 @@ ss_status tsb_test_resident_replay(int32_t n_units, int32_t capacity, int32_t po
   });
 }
 
+ss_status tsb_test_dg_layout(const ss_desc* d, const ss_plan* p, const ss_options* o, uint64_t* out, uint32_t n_out,
+                             uint32_t* residents, uint32_t cap) {
+  return guard([&] {
+    need(d && p && o && (out || !n_out) && (residents || !cap), "tsb_test_dg_layout: null argument");
+    const ss_options oo = versioned(o, options_defaults, "tsb_test_dg_layout options");
+    std::vector<uint32_t> res;
+    const std::vector<uint64_t> v = tsb::dg_layout_summary(d->d, p->p, oo, &res);
+    for (uint32_t i = 0; i < n_out && i < v.size(); ++i) out[i] = v[i];
+    for (uint32_t i = 0; i < cap && i < res.size(); ++i) residents[i] = res[i];
+  });
+}
+
 ss_status tsb_test_sha256(const void* data, uint64_t len, uint8_t* out) {
   return guard([&] {
     need((data || !len) && out, "tsb_test_sha256: null argument");

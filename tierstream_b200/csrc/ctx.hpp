@@ -90,6 +90,9 @@ class DgContext {
 
 struct PeerTier;
 // peer: the peer tier (peer.hpp), or null for pinned RAM only.
+// The device-gated layout of an open (no device work): the numbers of the layout test hook, the residents' keys.
+std::vector<uint64_t> dg_layout_summary(const Desc& d, const Plan& p, const ss_options& o,
+                                        std::vector<uint32_t>* residents);
 std::unique_ptr<DgContext> open_dg_context(const Desc& d, const Plan& p, const ss_options& o,
                                            const PeerTier* peer = nullptr);
 

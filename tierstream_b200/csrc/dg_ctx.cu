@@ -1860,6 +1860,18 @@ DeviceScope::~DeviceScope() {
   if (prev_ >= 0) cudaSetDevice(prev_);
 }
 
+// The device-gated layout of an open as numbers (the layout test hook): keys, R, D, B, P, Q, I, F, S, disk_queue,
+// blocks, persistent_slots, slots, guard_slot, unit_bytes, host_stride, disk_tier, disk_prefetch, scored, w_trans,
+// w_freq, w_rec, the resident count; then the residents' keys.
+std::vector<uint64_t> dg_layout_summary(const Desc& d, const Plan& p, const ss_options& o,
+                                        std::vector<uint32_t>* residents) {
+  const Layout x = make_layout(d, p, o, nullptr);
+  if (residents) *residents = x.residents;
+  return {x.keys, x.R, x.D, x.B, x.P, x.Q, x.I, x.F, x.S, x.disk_queue, x.blocks, x.persistent_slots, x.slots,
+          x.guard_slot, x.unit_bytes, x.host_stride, x.disk_tier, x.disk_prefetch, x.scored, x.w_trans, x.w_freq,
+          x.w_rec, x.residents.size()};
+}
+
 std::unique_ptr<DgContext> open_dg_context(const Desc& d, const Plan& p, const ss_options& o, const PeerTier* peer) {
   require(o.backend == SS_BACKEND_CUDA, SS_E_UNSUPPORTED,
           "device-gated: this build has the CUDA backend only (ss_options.backend = SS_BACKEND_CUDA)");
