@@ -217,3 +217,50 @@ extern "C" __attribute__((visibility("default"))) int oref_dg_layout(const char*
     return -1;
   }
 }
+
+// The reference's own descriptor parser and planner through its C ABI (capi.cpp): the descriptor (status, its JSON, every
+// layer's units and unit bytes), then a plan made from a budget and benefits (mode 0, ss_plan_make) or given tiers (mode
+// 1, ss_plan_from_tiers): every unit's tier, the totals and the plan's JSON. Returns the plan's status (or the
+// descriptor's when that failed, with *desc_status set).
+extern "C" __attribute__((visibility("default"))) int oref_plan(
+    const char* desc_json, size_t len, const ss_budget* budget, const double* benefit, size_t n_benefit,
+    const uint8_t* tiers, size_t n_tiers, int mode, uint8_t* tiers_out, size_t cap, ss_plan_totals* totals,
+    char* json_out, size_t json_cap, char* desc_out, size_t desc_cap, uint64_t* layer_out, size_t layer_cap,
+    int* desc_status, char* err, size_t errlen) {
+  ss_desc* d = nullptr;
+  *desc_status = ss_desc_from_json(desc_json, len, &d);
+  if (*desc_status != SS_OK) {
+    if (err && errlen) std::snprintf(err, errlen, "%s", ss_last_error());
+    return *desc_status;
+  }
+  void* text = nullptr;
+  size_t n = 0;
+  if (ss_desc_to_json(d, reinterpret_cast<char**>(&text), &n) == SS_OK) {
+    std::snprintf(desc_out, desc_cap, "%.*s", int(n), static_cast<const char*>(text));
+    ss_free(text);
+  }
+  const int L = ss_desc_n_layers(d);
+  for (int l = 0; l < L && size_t(2 * l + 1) < layer_cap; ++l) {
+    layer_out[2 * l] = uint64_t(ss_desc_layer_units(d, l));
+    layer_out[2 * l + 1] = ss_desc_unit_bytes(d, l);
+  }
+  ss_plan* p = nullptr;
+  const ss_status st = mode == 0 ? ss_plan_make(d, budget, benefit, n_benefit, &p)
+                                 : ss_plan_from_tiers(d, budget, tiers, n_tiers, &p);
+  if (st != SS_OK) {
+    if (err && errlen) std::snprintf(err, errlen, "%s", ss_last_error());
+    ss_desc_free(d);
+    return st;
+  }
+  size_t at = 0;
+  for (int l = 0; l < L; ++l)
+    for (int u = 0; u < ss_desc_layer_units(d, l) && at < cap; ++u) tiers_out[at++] = uint8_t(ss_plan_unit_tier(p, l, u));
+  ss_plan_get_totals(p, totals);
+  if (ss_plan_to_json(p, reinterpret_cast<char**>(&text), &n) == SS_OK) {
+    std::snprintf(json_out, json_cap, "%.*s", int(n), static_cast<const char*>(text));
+    ss_free(text);
+  }
+  ss_plan_free(p);
+  ss_desc_free(d);
+  return SS_OK;
+}
