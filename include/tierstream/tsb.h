@@ -141,6 +141,18 @@ SS_API ss_status tsb_test_file_read(const char* path, uint64_t offset, uint64_t 
 SS_API ss_status tsb_test_async_reads(const char* path, const uint64_t* offsets, uint32_t n, uint64_t bytes, void* dst,
                                       uint32_t threads, int reverse);
 
+/* Test hook: the open's fill pipeline on the host alone. Unit i is `unit_bytes` at offsets[i] of the file at `path`;
+ * targets[i] >= 0 lands it in slot targets[i] of `device` (a host area standing in for the arena, slots of unit_bytes
+ * rounded up to 4 KiB) through a ring of `buffers` buffers of `buffer_bytes`, copied by a copy engine of its own
+ * copy_delay_us after each batch was submitted; targets[i] < 0 reads it in place into block -1 - targets[i] of `host`.
+ * `readers` reader threads, unbuffered reads when direct is set and allowed. fail_batch >= 0: the copy engine refuses
+ * that batch (SS_E_BACKEND). stats[6] (may be null): slot units, in-place units, batches, buffers recycled for a
+ * waiting reader, reader waits for a buffer, batches in flight at most. */
+SS_API ss_status tsb_test_load(const char* path, const uint64_t* offsets, const int32_t* targets, uint32_t n,
+                               uint64_t unit_bytes, void* device, void* host, uint32_t buffers, uint64_t buffer_bytes,
+                               uint32_t readers, int direct, uint32_t copy_delay_us, int32_t fail_batch,
+                               uint64_t* stats);
+
 /* Test hook: a host-mode resident set (one layer) driven as the host forward mode drives it: n_place units placed at
  * the open (place_pin: pinned), then per step the routed units routed[step][k] (-1 = none) with flags[step][unit]
  * (bit 0: busy, in flight; bit 1: prefetched this forward, so neither a hit nor admitted, a miss for recency), one

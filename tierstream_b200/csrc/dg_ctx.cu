@@ -31,6 +31,7 @@
 #include "dg_core.hpp"
 #include "errors.hpp"
 #include "kernels.hpp"
+#include "loader.hpp"
 #include "peer.hpp"
 #include "pinned.hpp"
 #include "score_profile.hpp"
@@ -1259,7 +1260,7 @@ class CudaDgContext final : public DgContext {
   std::string stats_json() const override {
     ss_dg_stats s;
     stats(&s);
-    char buf[2048];
+    char buf[3072];
     std::snprintf(buf, sizeof buf,
                   "{\"schema\":\"strix-stream/stats-v1\",\"mode\":\"device-gated\",\"copy\":\"%s\","
                   "\"dg\":{\"tokens\":%llu,\"lookups\":%llu,\"misses\":%llu,\"covered\":%llu,\"fetched\":%llu,"
@@ -1269,7 +1270,11 @@ class CudaDgContext final : public DgContext {
                   "\"disk_read_ns\":%llu,\"disk_drops\":%llu,\"disk_discards\":%llu,\"disk_units\":%llu},"
                   "\"peer\":{\"world\":%u,\"rank\":%d,"
                   "\"all_owned\":%d,\"copy\":\"%s\",\"peer_units\":%llu,\"self_units\":%llu},"
-                  "\"open\":{\"alloc_s\":%.3f,\"fill_pinned_s\":%.3f,\"fill_residents_s\":%.3f,\"verify_s\":%.3f}}",
+                  "\"open\":{\"alloc_s\":%.3f,\"alloc_arena_s\":%.3f,\"alloc_pinned_s\":%.3f,\"place_s\":%.3f,"
+                  "\"fill_s\":%.3f,\"fill_pinned_s\":%.3f,\"fill_residents_s\":%.3f,\"verify_s\":%.3f,"
+                  "\"load\":\"%s\",\"load_readers\":%u,\"load_buffers\":%u,\"load_buffer_bytes\":%llu,"
+                  "\"load_batches\":%llu,\"load_slot_units\":%llu,\"load_pinned_units\":%llu,"
+                  "\"load_reader_waits\":%llu,\"load_recycles\":%llu,\"load_residents_submitted_s\":%.3f}}",
                   mover_->kernel_copies() ? "land-kernel" : "copy-engine", (unsigned long long)s.tokens,
                   (unsigned long long)s.lookups, (unsigned long long)s.misses, (unsigned long long)s.covered,
                   (unsigned long long)s.fetched, (unsigned long long)s.prefetched, (unsigned long long)s.bank_serves,
@@ -1282,7 +1287,11 @@ class CudaDgContext final : public DgContext {
                   (unsigned long long)s.disk_units, peer_ ? peer_->world : 0u, peer_ ? peer_->rank : -1,
                   peer_ && peer_->all_owned ? 1 : 0, peer_ && peer_->copy == 1 ? "copy-engine" : "land-kernel",
                   (unsigned long long)mover_->peer_units(), (unsigned long long)mover_->self_units(), open_alloc_s_,
-                  open_fill_pinned_s_, open_fill_res_s_, open_verify_s_);
+                  open_arena_s_, open_pinned_s_, open_cache_s_, open_fill_s_, open_fill_pinned_s_, open_fill_res_s_,
+                  open_verify_s_, load_serial_ ? "serial" : "pipeline", load_readers_, load_buffers_,
+                  (unsigned long long)load_buffer_bytes_, (unsigned long long)load_.batches,
+                  (unsigned long long)load_.slot_units, (unsigned long long)load_.host_units,
+                  (unsigned long long)load_.reader_waits, (unsigned long long)load_.recycles, load_.slot_seconds);
     return buf;
   }
   void reset_open() override {
@@ -1470,6 +1479,7 @@ class CudaDgContext final : public DgContext {
       bufs_.arena.push_back(static_cast<char*>(a));
       ck(cudaMemset(static_cast<char*>(a) + uint64_t(x_.guard_slot) * pb, 0, size_t(pb)), "cudaMemset (guard slot)");
     }
+    const auto t_arena = Clock::now();
     ck(cudaMalloc(reinterpret_cast<void**>(&bufs_.slot_of), size_t(x_.keys) * 4), "cudaMalloc (slot table)");
     const size_t ctl_words = 8 + 2 * size_t(G) + (G + 1) + 4;
     ck(cudaMalloc(reinterpret_cast<void**>(&ctl_), ctl_words * 4), "cudaMalloc (controls)");
@@ -1548,7 +1558,10 @@ class CudaDgContext final : public DgContext {
       chunk_bytes.push_back(size_t(chunk_units.back() * hs));
       left -= chunk_units.back();
     }
+    const auto t_pinned0 = Clock::now();
     pinned_ = alloc_pinned(chunk_bytes, device_);
+    open_pinned_s_ = std::chrono::duration<double>(Clock::now() - t_pinned0).count();
+    open_arena_s_ = std::chrono::duration<double>(t_arena - t_start).count();
     for (const PinnedChunk& c : pinned_) chunks_.push_back(c.ptr);
     for (size_t c = 0; c < chunks_.size(); ++c) {
       void* pd = nullptr;
@@ -1632,9 +1645,11 @@ class CudaDgContext final : public DgContext {
     o_.dg_seed_n = 0;
     order.insert(order.end(), x_.residents.begin(), x_.residents.end());
     for (uint32_t k = 0; k < x_.keys; ++k) order.push_back(k);
+    const auto t_place = Clock::now();
     core_->place(order, x_.disk_tier ? &x_.disk : nullptr);
     if (!x_.profile.empty()) core_->load_counts(x_.profile);
     open_alloc_s_ = std::chrono::duration<double>(Clock::now() - t_start).count();
+    open_cache_s_ = std::chrono::duration<double>(Clock::now() - t_place).count();
     fill();
     mover_->upload_table(core_->table().data(), x_.keys);
     core_->check();
@@ -1648,34 +1663,138 @@ class CudaDgContext final : public DgContext {
     open_seconds_ = std::chrono::duration<double>(Clock::now() - t_start).count();
   }
 
-  // The open's fill: every unit's bytes from its file into its slot or block, by a pool of reader threads. A resident
-  // lands through a pinned staging ring; with verify_hash and descriptor hashes, pinned units are hashed on the host
-  // and residents on the device (one K3 launch over every resident slot) before the first token.
+  // The open's fill: every unit's bytes from its file into its slot or block; with verify_hash and descriptor hashes,
+  // pinned units are hashed on the host as they are read and residents on the device (one K3 launch over every
+  // resident slot) before the first token. By default a pipeline (loader.hpp): reader threads read the residents into
+  // a ring of pinned buffers, whose copies this thread enqueues as each buffer is full, and the pinned units in place
+  // in between, so the reads, the host link and the pinned units' reads overlap (the reference's startup loader,
+  // src/dg_ctx.cpp:1953-2016). TSB_LOAD_SERIAL=1 selects the phased order instead (pinned units, then residents in
+  // rounds of reads and copies; the reference's DG_LOAD_SERIAL); TSB_LOAD_READERS (1-32, default 8), TSB_LOAD_BUFFERS
+  // (1-16, default 4) and TSB_LOAD_BUFFER_MIB (1-1024, default 64, at least one unit) size the pipeline.
   void fill() {
     const auto t_fill = Clock::now();
     const uint32_t G = uint32_t(x_.gated.size());
     std::vector<std::pair<uint32_t, uint32_t>> res, pin, from_store;  // (g, unit)
+    std::vector<LoadUnit> units;  // every resident and pinned unit read from its file, in key order
     for (uint32_t g = 0; g < G; ++g)
       for (uint32_t u = 0; u < core_->units(g); ++u) {
         const uint32_t k = core_->key(g, u);
         const bool owned = peer_ && peer_->owned(k);  // an owned unit's block is never read: not filled
-        if (core_->slot_of(k) >= 0) (owned ? from_store : res).push_back({g, u});
-        else if (!owned && core_->block_of(k) >= 0) pin.push_back({g, u});  // (a file home stays in its file)
+        if (core_->slot_of(k) >= 0) {
+          (owned ? from_store : res).push_back({g, u});
+          if (!owned) units.push_back(LoadUnit{x_.gated[g], int(u), core_->slot_of(k), nullptr});
+        } else if (!owned && core_->block_of(k) >= 0) {  // (a file home stays in its file)
+          pin.push_back({g, u});
+          units.push_back(LoadUnit{x_.gated[g], int(u), -1, bufs_.blocks[size_t(core_->block_of(k))]});
+        }
       }
+    const bool serial = std::getenv("TSB_LOAD_SERIAL") && std::atoi(std::getenv("TSB_LOAD_SERIAL")) != 0;
+    if (serial) fill_serial(res, pin);
+    else fill_pipeline(units, res.size());
+    load_serial_ = serial;
+    cudaStream_t fs = mover_->stream(Mover::kDem);
+    // owned residents from their stores (the stores were checked against the hashes when they were filled)
+    for (const auto& [g, u] : from_store) {
+      const uint32_t k = core_->key(g, u);
+      const char* src = peer_->src(k, x_.unit_bytes);
+      for (size_t p = 0; p < x_.part_bytes.size(); ++p)
+        ck(cudaMemcpyAsync(unit_part_dst(core_->slot_of(k), uint32_t(p)), src + x_.part_offset[p],
+                           size_t(x_.part_bytes[p]), cudaMemcpyDefault, fs),
+           "cudaMemcpyAsync (fill from store)");
+    }
+    ck(cudaStreamSynchronize(fs), "cudaStreamSynchronize (fill from store)");
+    res.insert(res.end(), from_store.begin(), from_store.end());
+    const auto t_res = Clock::now();
+    if (o_.verify_hash && !res.empty() && !d_.layers[size_t(x_.gated[0])].hash.empty()) verify_residents(res);
+    open_fill_s_ = std::chrono::duration<double>(t_res - t_fill).count();
+    open_verify_s_ = std::chrono::duration<double>(Clock::now() - t_res).count();
+  }
+
+  // One environment count in [lo, hi], else the default (a value out of range is refused).
+  static unsigned env_count(const char* name, unsigned def, unsigned lo, unsigned hi) {
+    const char* e = std::getenv(name);
+    if (!e || !*e) return def;
+    char* end = nullptr;
+    const long v = std::strtol(e, &end, 10);
+    require(end && *end == 0 && v >= long(lo) && v <= long(hi), SS_E_INVALID,
+            std::string("device-gated: invalid ") + name + " (" + std::to_string(lo) + "-" + std::to_string(hi) + ")");
+    return unsigned(v);
+  }
+
+  void fill_pipeline(const std::vector<LoadUnit>& units, size_t n_res) {
+    const uint64_t hs = x_.host_stride;
+    const unsigned readers = env_count("TSB_LOAD_READERS", 8, 1, 32);
+    unsigned nbuf = env_count("TSB_LOAD_BUFFERS", 4, 1, 16);
+    const uint64_t target = uint64_t(env_count("TSB_LOAD_BUFFER_MIB", 64, 1, 1024)) << 20;
+    // a buffer holds whole units (at least one), never more than the residents need
+    const uint64_t per = std::max<uint64_t>(1, std::min<uint64_t>(target / hs, std::max<size_t>(n_res, 1)));
+    const uint64_t batches = (uint64_t(n_res) + per - 1) / per;
+    nbuf = unsigned(std::min<uint64_t>(nbuf, batches));
+    struct Ring {
+      std::vector<char*> buf;
+      std::vector<cudaEvent_t> ev;
+      cudaStream_t s = nullptr;
+      ~Ring() {
+        if (s) (void)cudaStreamSynchronize(s);  // (an error path: no copy may read a buffer being freed)
+        for (char* b : buf) (void)cudaFreeHost(b);
+        for (cudaEvent_t e : ev) (void)cudaEventDestroy(e);
+      }
+    } ring;
+    ring.s = mover_->stream(Mover::kDem);
+    for (unsigned b = 0; b < nbuf; ++b) {
+      char* p = nullptr;
+      ck(cudaHostAlloc(reinterpret_cast<void**>(&p), size_t(per * hs), cudaHostAllocPortable), "cudaHostAlloc (load ring)");
+      ring.buf.push_back(p);
+      cudaEvent_t e = nullptr;
+      ck(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "cudaEventCreate (load ring)");
+      ring.ev.push_back(e);
+    }
+    const bool verify = o_.verify_hash != 0;
+    const LoadStats st = run_load(
+        units, ring.buf, per * hs, hs, readers,
+        [&](const LoadUnit& lu, char* dst) {  // a reader thread: file reads and hashes only
+          read_unit(lu.layer, lu.unit, dst);
+          const Layer& l = d_.layers[size_t(lu.layer)];
+          if (lu.slot < 0 && verify && !l.hash.empty())
+            require(xxh64(dst, size_t(x_.unit_bytes)) == l.hash[size_t(lu.unit)], SS_E_HASH,
+                    "device-gated: unit (" + std::to_string(lu.layer) + ", " + std::to_string(lu.unit) +
+                        ") differs from its descriptor hash");
+        },
+        [&](size_t b, const std::vector<LoadCopy>& copies) {  // this thread: the batch's copies, then its event
+          for (const LoadCopy& c : copies)
+            for (size_t p = 0; p < x_.part_bytes.size(); ++p)
+              ck(cudaMemcpyAsync(unit_part_dst(c.slot, uint32_t(p)), c.data + x_.part_offset[p],
+                                 size_t(x_.part_bytes[p]), cudaMemcpyHostToDevice, ring.s),
+                 "cudaMemcpyAsync (load)");
+          ck(cudaEventRecord(ring.ev[b], ring.s), "cudaEventRecord (load ring)");
+        },
+        [&](size_t b) { ck(cudaEventSynchronize(ring.ev[b]), "cudaEventSynchronize (load ring)"); });
+    ck(cudaStreamSynchronize(ring.s), "cudaStreamSynchronize (load)");
+    load_ = st;
+    load_readers_ = readers;
+    load_buffers_ = nbuf;
+    load_buffer_bytes_ = per * hs;
+  }
+
+  // The phased fill: the pinned units by a pool of reader threads, then the residents through a ring of pinned staging
+  // units, read a ringful at a time and copied before the next round of reads.
+  void fill_serial(const std::vector<std::pair<uint32_t, uint32_t>>& res,
+                   const std::vector<std::pair<uint32_t, uint32_t>>& pin) {
+    const auto t_fill = Clock::now();
     const bool verify = o_.verify_hash != 0;
     unsigned nthreads = std::max(1u, std::min(16u, std::thread::hardware_concurrency()));
     std::atomic<size_t> next{0};
     std::mutex err_mu;
-    std::string err;
+    std::exception_ptr err;  // the first failure, with its status (SS_E_IO, SS_E_HASH)
     auto worker = [&](auto&& job, size_t n) {
       for (;;) {
         const size_t i = next.fetch_add(1);
         if (i >= n) return;
         try {
           job(i);
-        } catch (const std::exception& e) {
+        } catch (...) {
           std::lock_guard<std::mutex> lk(err_mu);
-          if (err.empty()) err = e.what();
+          if (!err) err = std::current_exception();
         }
       }
     };
@@ -1684,7 +1803,7 @@ class CudaDgContext final : public DgContext {
       std::vector<std::thread> th;
       for (unsigned t = 0; t < nthreads; ++t) th.emplace_back([&] { worker(job, n); });
       for (auto& t : th) t.join();
-      if (!err.empty()) fail(SS_E_IO, err);
+      if (err) std::rethrow_exception(err);
     };
     auto hash_of = [&](uint32_t g, uint32_t u) -> const uint64_t* {
       const Layer& l = d_.layers[size_t(x_.gated[g])];
@@ -1727,22 +1846,8 @@ class CudaDgContext final : public DgContext {
       throw;
     }
     for (char* s : stage) cudaFreeHost(s);
-    // owned residents from their stores (the stores were checked against the hashes when they were filled)
-    for (const auto& [g, u] : from_store) {
-      const uint32_t k = core_->key(g, u);
-      const char* src = peer_->src(k, x_.unit_bytes);
-      for (size_t p = 0; p < x_.part_bytes.size(); ++p)
-        ck(cudaMemcpyAsync(unit_part_dst(core_->slot_of(k), uint32_t(p)), src + x_.part_offset[p],
-                           size_t(x_.part_bytes[p]), cudaMemcpyDefault, fs),
-           "cudaMemcpyAsync (fill from store)");
-    }
-    ck(cudaStreamSynchronize(fs), "cudaStreamSynchronize (fill from store)");
-    res.insert(res.end(), from_store.begin(), from_store.end());
-    const auto t_res = Clock::now();
-    if (verify && !res.empty() && hash_of(0, 0)) verify_residents(res);
     open_fill_pinned_s_ = std::chrono::duration<double>(t_pinned - t_fill).count();
-    open_fill_res_s_ = std::chrono::duration<double>(t_res - t_pinned).count();
-    open_verify_s_ = std::chrono::duration<double>(Clock::now() - t_res).count();
+    open_fill_res_s_ = std::chrono::duration<double>(Clock::now() - t_pinned).count();
   }
 
   // K3 over every resident slot at once: the arena's bytes against the descriptor's hashes.
@@ -1843,6 +1948,11 @@ class CudaDgContext final : public DgContext {
   ss_dg_boundary_timeline boundary_{};
   std::vector<double> gpu_wait_us_, gpu_ready_us_;
   double open_seconds_ = 0, open_alloc_s_ = 0, open_fill_pinned_s_ = 0, open_fill_res_s_ = 0, open_verify_s_ = 0;
+  double open_fill_s_ = 0, open_arena_s_ = 0, open_pinned_s_ = 0, open_cache_s_ = 0;
+  bool load_serial_ = false;
+  LoadStats load_;
+  unsigned load_readers_ = 0, load_buffers_ = 0;
+  uint64_t load_buffer_bytes_ = 0;
 };
 
 }  // namespace

@@ -1,14 +1,21 @@
 // The tsb_* entry points of include/tierstream/tsb.h.
 #include <cuda_runtime.h>
 
+#include <chrono>
+#include <condition_variable>
+#include <cstdlib>
 #include <cstring>
+#include <deque>
 #include <memory>
+#include <mutex>
+#include <thread>
 #include <string>
 #include <vector>
 
 #include "dg_core.hpp"
 #include "errors.hpp"
 #include "kernels.hpp"
+#include "loader.hpp"
 #include "source_file.hpp"
 #include "tierstream/tsb.h"
 #include "xxh64.hpp"
@@ -173,6 +180,94 @@ ss_status tsb_test_async_reads(const char* path, const uint64_t* offsets, uint32
       }
     }
     if (first) std::rethrow_exception(first);
+  });
+}
+
+ss_status tsb_test_load(const char* path, const uint64_t* offsets, const int32_t* targets, uint32_t n,
+                        uint64_t unit_bytes, void* device, void* host, uint32_t buffers, uint64_t buffer_bytes,
+                        uint32_t readers, int direct, uint32_t copy_delay_us, int32_t fail_batch, uint64_t* stats) {
+  return run([&] {
+    tsb::require(path && (offsets || !n) && (targets || !n) && unit_bytes >= 1 && readers >= 1 && readers <= 64 &&
+                     buffers <= 64,
+                 SS_E_INVALID, "tsb_test_load: bad argument");
+    const uint64_t stride = (unit_bytes + 4095) / 4096 * 4096;
+    tsb::SourceFile f(path, 4096, direct != 0);
+    std::vector<tsb::LoadUnit> units(n);
+    for (uint32_t i = 0; i < n; ++i) {
+      units[i].unit = int(i);
+      units[i].slot = targets[i];
+      if (targets[i] < 0) {
+        tsb::require(host != nullptr, SS_E_INVALID, "tsb_test_load: a host unit and no host area");
+        units[i].host = static_cast<char*>(host) + uint64_t(-int64_t(targets[i]) - 1) * stride;
+      } else {
+        tsb::require(device != nullptr, SS_E_INVALID, "tsb_test_load: a slot unit and no device area");
+      }
+    }
+    struct Ring {
+      std::vector<char*> p;
+      ~Ring() {
+        for (char* b : p) std::free(b);
+      }
+    } ring;
+    for (uint32_t b = 0; b < buffers; ++b) {
+      ring.p.push_back(static_cast<char*>(std::aligned_alloc(4096, size_t((buffer_bytes + 4095) / 4096 * 4096))));
+      tsb::require(ring.p.back() != nullptr, SS_E_NOMEM, "tsb_test_load: ring buffer");
+    }
+    // a copy engine of its own: copies run in submission order on one thread, copy_delay_us after they were submitted,
+    // and a buffer's event completes when its last copy did
+    std::mutex mu;
+    std::condition_variable cv;
+    std::deque<std::pair<uint64_t, std::vector<tsb::LoadCopy>>> q;
+    std::vector<uint64_t> event(buffers, 0);
+    uint64_t seq = 0, completed = 0, batch = 0;
+    bool stop = false;
+    std::thread engine([&] {
+      std::unique_lock<std::mutex> lk(mu);
+      for (;;) {
+        cv.wait(lk, [&] { return stop || !q.empty(); });
+        if (q.empty()) return;
+        auto job = std::move(q.front());
+        q.pop_front();
+        lk.unlock();
+        if (copy_delay_us) std::this_thread::sleep_for(std::chrono::microseconds(copy_delay_us));
+        for (const tsb::LoadCopy& c : job.second)
+          std::memcpy(static_cast<char*>(device) + uint64_t(c.slot) * stride, c.data, size_t(unit_bytes));
+        lk.lock();
+        completed = job.first;
+        cv.notify_all();
+      }
+    });
+    tsb::LoadStats st;
+    std::exception_ptr err;
+    try {
+      st = tsb::run_load(
+          units, ring.p, buffer_bytes, stride, readers,
+          [&](const tsb::LoadUnit& u, char* dst) { f.read(dst, offsets[u.unit], unit_bytes); },
+          [&](size_t buf, const std::vector<tsb::LoadCopy>& copies) {
+            std::lock_guard<std::mutex> lk(mu);
+            tsb::require(int32_t(batch++) != fail_batch, SS_E_BACKEND, "tsb_test_load: the copy engine refused");
+            q.emplace_back(++seq, copies);
+            event[buf] = seq;
+            cv.notify_all();
+          },
+          [&](size_t buf) {
+            std::unique_lock<std::mutex> lk(mu);
+            cv.wait(lk, [&] { return completed >= event[buf]; });
+          });
+    } catch (...) {
+      err = std::current_exception();
+    }
+    {
+      std::lock_guard<std::mutex> lk(mu);
+      stop = true;
+      cv.notify_all();
+    }
+    engine.join();
+    if (err) std::rethrow_exception(err);
+    if (stats) {
+      const uint64_t v[6] = {st.slot_units, st.host_units, st.batches, st.recycles, st.reader_waits, st.max_in_flight};
+      std::memcpy(stats, v, sizeof v);
+    }
   });
 }
 
