@@ -14,6 +14,7 @@
 #include "ctx.hpp"
 #include "errors.hpp"
 #include "kernels.hpp"
+#include "loader.hpp"
 #include "peer.hpp"
 #include "source_file.hpp"
 
@@ -114,51 +115,54 @@ PeerStore::PeerStore(const Desc& d, const std::vector<int32_t>& owner, int32_t r
   try {
     std::vector<std::unique_ptr<SourceFile>> files;
     for (const Source& s : d.sources) files.push_back(std::make_unique<SourceFile>(s.path, s.align, false));
-    auto read_unit = [&](uint32_t g, uint32_t u, char* dst) {
-      const Layer& l = d.layers[size_t(gk.layers[g])];
-      uint64_t off = 0;
-      for (const Part& p : l.parts) {
-        files[size_t(p.source)]->read(dst + off, p.offset + uint64_t(u) * p.stride, p.bytes);
-        off += p.bytes;
-      }
-    };
-    // a ring of pinned staging units, one reader thread each; copies on one stream, the ring reused after a sync
-    const unsigned nthreads = std::max(1u, std::min(16u, std::thread::hardware_concurrency()));
-    const size_t ring = std::min<size_t>(units_, nthreads);
-    std::vector<char*> stage(ring, nullptr);
+    // the owned units through the open's fill pipeline (loader.hpp): reader threads read them into a ring of pinned
+    // buffers (4 of up to 64 MiB), and this thread copies each full buffer into the store on one stream
+    const uint64_t stride = (gk.unit_bytes + 4095) / 4096 * 4096;
+    const uint64_t per = std::max<uint64_t>(1, std::min<uint64_t>((uint64_t(64) << 20) / stride, units_));
+    const size_t nbuf = size_t(std::min<uint64_t>(4, (units_ + per - 1) / per));
+    std::vector<char*> stage;
+    std::vector<cudaEvent_t> ev;
     cudaStream_t s = nullptr;
     auto release = [&] {
-      for (char* p : stage)
-        if (p) cudaFreeHost(p);
+      if (s) (void)cudaStreamSynchronize(s);  // (an error path: no copy may read a buffer being freed)
+      for (char* p : stage) cudaFreeHost(p);
+      for (cudaEvent_t e : ev) cudaEventDestroy(e);
       if (s) cudaStreamDestroy(s);
     };
     try {
-      for (auto& p : stage)
-        ck(cudaHostAlloc(reinterpret_cast<void**>(&p), size_t(gk.unit_bytes), cudaHostAllocPortable),
-           "cudaHostAlloc (peer store staging)");
       ck(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking), "cudaStreamCreate (peer store)");
-      std::mutex err_mu;
-      std::string err;
-      for (size_t first = 0; first < units_; first += ring) {
-        const size_t n = std::min(ring, size_t(units_) - first);
-        std::vector<std::thread> th;
-        for (size_t i = 0; i < n; ++i)
-          th.emplace_back([&, i] {
-            try {
-              read_unit(mine[first + i].first, mine[first + i].second, stage[i]);
-            } catch (const std::exception& e) {
-              std::lock_guard<std::mutex> lk(err_mu);
-              if (err.empty()) err = e.what();
-            }
-          });
-        for (auto& t : th) t.join();
-        if (!err.empty()) fail(SS_E_IO, "peer tier: " + err);
-        for (size_t i = 0; i < n; ++i)
-          ck(cudaMemcpyAsync(base_ + (first + i) * gk.unit_bytes, stage[i], size_t(gk.unit_bytes),
-                             cudaMemcpyHostToDevice, s),
-             "cudaMemcpyAsync (peer store fill)");
-        ck(cudaStreamSynchronize(s), "cudaStreamSynchronize (peer store fill)");
+      for (size_t b = 0; b < nbuf; ++b) {
+        char* p = nullptr;
+        ck(cudaHostAlloc(reinterpret_cast<void**>(&p), size_t(per * stride), cudaHostAllocPortable),
+           "cudaHostAlloc (peer store staging)");
+        stage.push_back(p);
+        cudaEvent_t e = nullptr;
+        ck(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "cudaEventCreate (peer store)");
+        ev.push_back(e);
       }
+      std::vector<LoadUnit> units(mine.size());
+      for (size_t i = 0; i < mine.size(); ++i)
+        units[i] = LoadUnit{gk.layers[mine[i].first], int(mine[i].second), int32_t(i), nullptr};  // slot = store index
+      const unsigned readers = std::max(1u, std::min(8u, std::thread::hardware_concurrency()));
+      run_load(
+          units, stage, per * stride, stride, readers,
+          [&](const LoadUnit& lu, char* dst) {
+            const Layer& l = d.layers[size_t(lu.layer)];
+            uint64_t off = 0;
+            for (const Part& p : l.parts) {
+              files[size_t(p.source)]->read(dst + off, p.offset + uint64_t(lu.unit) * p.stride, p.bytes);
+              off += p.bytes;
+            }
+          },
+          [&](size_t b, const std::vector<LoadCopy>& copies) {
+            for (const LoadCopy& c : copies)
+              ck(cudaMemcpyAsync(base_ + uint64_t(c.slot) * gk.unit_bytes, c.data, size_t(gk.unit_bytes),
+                                 cudaMemcpyHostToDevice, s),
+                 "cudaMemcpyAsync (peer store fill)");
+            ck(cudaEventRecord(ev[b], s), "cudaEventRecord (peer store fill)");
+          },
+          [&](size_t b) { ck(cudaEventSynchronize(ev[b]), "cudaEventSynchronize (peer store fill)"); });
+      ck(cudaStreamSynchronize(s), "cudaStreamSynchronize (peer store fill)");
       // the store against the descriptor's hashes: K3 over every unit, in launches of up to 4096 units
       const bool hashes = !d.layers[size_t(gk.layers[0])].hash.empty();
       if (verify && hashes) {
