@@ -116,6 +116,8 @@ typedef struct tsb_dg_replay_config {
   const uint32_t* mr_count;
   const uint32_t* mr_ids;
   uint64_t* mstats;
+  /* sstats (optional): [tokens][5] score_fallbacks, scored_victims, score_layers, score_candidates, score_saturated */
+  uint64_t* sstats;
 } tsb_dg_replay_config;
 SS_API ss_status tsb_test_dg_replay(const tsb_dg_replay_config* cfg, const int32_t* ids, const int32_t* preds,
                                     int32_t* tables, uint64_t* stats, const uint8_t* src_units, uint64_t* read_sum);

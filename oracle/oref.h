@@ -59,6 +59,8 @@ typedef struct oref_dg_config {
   const uint32_t* mr_count;
   const uint32_t* mr_ids;
   uint64_t* mstats;
+  /* sstats (optional): [tokens][5] score_fallbacks, scored_victims, score_layers, score_candidates, score_saturated */
+  uint64_t* sstats;
 } oref_dg_config;
 #define OREF_NXSTATS 6
 

@@ -261,6 +261,12 @@ extern "C" __attribute__((visibility("default"))) int oref_dg_replay(const oref_
         const uint64_t mv[4] = {q.resident_units, q.resident_evicted, q.mkres_file_reads, q.mkres_wb_bytes};
         std::memcpy(c->mstats + size_t(tok) * 4, mv, sizeof mv);
       }
+      if (c->sstats) {
+        const ts::DgStats& q = core.stats();
+        const uint64_t sv[5] = {q.score_fallbacks, q.scored_victims, q.score_layers, q.score_candidates,
+                                q.score_saturated};
+        std::memcpy(c->sstats + size_t(tok) * 5, sv, sizeof sv);
+      }
       if (c->qstats) {
         const ts::DgStats& q = core.stats();
         const uint64_t qv[4] = {q.disk_overlapped, q.disk_max_in_flight, q.disk_carried, q.disk_carried_bytes};

@@ -37,15 +37,17 @@ CASES = {
 
 
 def _compare(cfg, ids, preds, xstats=False):
+    """Tables, the 16 counters and the five score counters (fallbacks, scored victims, layers scored, candidates,
+    saturated) after every token, and the file tier's counters with xstats."""
+    x_ref = np.zeros((cfg.tokens, 6), dtype=np.uint64) if xstats else None
+    x_new = np.zeros((cfg.tokens, 6), dtype=np.uint64) if xstats else None
+    q_ref = np.zeros((cfg.tokens, 5), dtype=np.uint64)
+    q_new = np.zeros((cfg.tokens, 5), dtype=np.uint64)
+    t_ref, s_ref = oracle.ref_replay(cfg, ids, preds, xstats=x_ref, sstats=q_ref)
+    t_new, s_new = runtime.replay(cfg, ids, preds, xstats=x_new, sstats=q_new)
     if xstats:
-        x_ref = np.zeros((cfg.tokens, 6), dtype=np.uint64)
-        x_new = np.zeros((cfg.tokens, 6), dtype=np.uint64)
-        t_ref, s_ref = oracle.ref_replay(cfg, ids, preds, xstats=x_ref)
-        t_new, s_new = runtime.replay(cfg, ids, preds, xstats=x_new)
         assert np.array_equal(x_new, x_ref)
-    else:
-        t_ref, s_ref = oracle.ref_replay(cfg, ids, preds)
-        t_new, s_new = runtime.replay(cfg, ids, preds)
+    assert np.array_equal(q_new, q_ref), "score counters differ: %s vs %s" % (q_new[-1].tolist(), q_ref[-1].tolist())
     for t in range(cfg.tokens):
         assert np.array_equal(t_new[t], t_ref[t]), "slot table differs after token %d" % t
         assert np.array_equal(s_new[t], s_ref[t]), "counters differ after token %d: %s vs %s" % (

@@ -220,6 +220,12 @@ void dg_replay(const tsb_dg_replay_config* c, const int32_t* ids, const int32_t*
       const uint64_t mv[4] = {q.resident_units, q.resident_evicted, q.mkres_file_reads, q.mkres_wb_bytes};
       std::memcpy(c->mstats + size_t(t) * 4, mv, sizeof mv);
     }
+    if (c->sstats) {
+      const CacheStats& q = core.stats();
+      const uint64_t sv[5] = {q.score_fallbacks, q.scored_victims, q.score_layers, q.score_candidates,
+                              q.score_saturated};
+      std::memcpy(c->sstats + size_t(t) * 5, sv, sizeof sv);
+    }
     if (c->qstats) {
       const CacheStats& q = core.stats();
       const uint64_t qv[4] = {q.disk_overlapped, q.disk_max_in_flight, q.disk_carried, q.disk_carried_bytes};

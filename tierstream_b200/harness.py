@@ -12,15 +12,15 @@ import torch
 from . import abi, runtime, synth
 
 
-class DgRun:
+class DgSetup:
+    """What DgRun opens: the descriptor, the plan (tiers: resident_keys, disk_keys, the rest pinned), the budget and the
+    options, built without a device (a CPU test checks the layout they give, tsb_test_dg_layout)."""
+
     def __init__(self, model, residents_per_layer=None, resident_keys=None, spare_per_layer=1, max_ids=2,
                  host_spare_units=None, diag=False, test_hooks=True, wb_defer=1, wb_stream=1, verify=False,
-                 n_pred=0, slices=64, mode=0, timeout_ms=10000, device_bytes=None, with_reader=True,
-                 resident_order=None, inclusive=0, peer=None, disk_keys=(), disk_staging=0, disk_prefetch=0, disk_queue=0,
-                 policy=0, weights=None, profile=None):
-        self.model = model
+                 timeout_ms=10000, device_bytes=None, resident_order=None, inclusive=0, disk_keys=(), disk_staging=0,
+                 disk_prefetch=0, disk_queue=0, policy=0, weights=None, profile=None):
         G, U = model.layers, model.units
-        self.G, self.U, self.n_ids, self.n_pred = G, U, max_ids, n_pred
         tiers = [abi.SS_TIER_PINNED] * (G * U)
         if resident_keys is None:
             resident_keys = []
@@ -31,6 +31,7 @@ class DgRun:
             tiers[k] = abi.SS_TIER_RESIDENT
         for k in disk_keys:  # the file tier: these units live in their files only
             tiers[k] = abi.SS_TIER_DISK
+        self.tiers = tiers
         self.resident_keys = list(resident_keys)
         self.disk_keys = list(disk_keys)
         b = abi.budget_defaults()
@@ -71,6 +72,18 @@ class DgRun:
             o.dg_disk_staging = disk_staging
             o.dg_disk_prefetch = disk_prefetch
             o.dg_disk_queue = disk_queue
+        self.budget, self.options = b, o
+
+
+class DgRun:
+    def __init__(self, model, n_pred=0, slices=64, mode=0, with_reader=True, peer=None, max_ids=2, **setup):
+        self.model = model
+        G, U = model.layers, model.units
+        self.G, self.U, self.n_ids, self.n_pred = G, U, max_ids, n_pred
+        s = DgSetup(model, max_ids=max_ids, **setup)
+        self.setup = s
+        self.desc, self.plan, o = s.desc, s.plan, s.options
+        self.resident_keys, self.disk_keys = s.resident_keys, s.disk_keys
         o.device = torch.cuda.current_device()  # the context lives on the engine's device
         self.ctx = runtime.DgContext(self.desc, self.plan, o, peer=peer)
         self.stream = torch.cuda.Stream()

@@ -310,7 +310,7 @@ def replay_config(n_units, part_bytes, persistent_slots, bank_slots, blocks, spa
 
 
 def replay(cfg, ids, preds=None, src_units=None, want_reads=False, xstats=None, rstats=None, pstats=None,
-           qstats=None, mstats=None):
+           qstats=None, mstats=None, sstats=None):
     """This library's deterministic replay (tsb_test_dg_replay): (tables, stats[, read_sum]). xstats: an optional
     uint64 array [tokens][6] filled with the file tier's counters after each boundary."""
     keys = sum(cfg.n_units[i] for i in range(cfg.n_gated))
@@ -319,6 +319,7 @@ def replay(cfg, ids, preds=None, src_units=None, want_reads=False, xstats=None, 
     cfg.pstats = pstats.ctypes.data_as(C.POINTER(C.c_uint64)) if pstats is not None else None  # [tokens][5]
     cfg.qstats = qstats.ctypes.data_as(C.POINTER(C.c_uint64)) if qstats is not None else None  # [tokens][4]
     cfg.mstats = mstats.ctypes.data_as(C.POINTER(C.c_uint64)) if mstats is not None else None  # [tokens][4]
+    cfg.sstats = sstats.ctypes.data_as(C.POINTER(C.c_uint64)) if sstats is not None else None  # [tokens][5]
     ids = np.ascontiguousarray(ids, dtype=np.int32)
     tables = np.empty((cfg.tokens, keys), dtype=np.int32)
     stats = np.empty((cfg.tokens, 16), dtype=np.uint64)
