@@ -122,6 +122,22 @@ typedef struct tsb_dg_replay_config {
 SS_API ss_status tsb_test_dg_replay(const tsb_dg_replay_config* cfg, const int32_t* ids, const int32_t* preds,
                                     int32_t* tables, uint64_t* stats, const uint8_t* src_units, uint64_t* read_sum);
 
+/* Test hook: the same configuration and trace driven as the context drives it, with the device's concurrency on the
+ * host: three copy streams as worker threads running their copies, entry and ready writes, event records and waits in
+ * order after random delays of up to delay_us (seeded), reads in flight landing on their own threads, and an engine
+ * thread that exports each layer from the device table as it is, waits for the layer's ready word when its export saw
+ * a miss, and reads every routed unit through the device table before it exports the next layer. src_units (required)
+ * holds every unit's bytes (unit-major); read_sum[tokens][n_gated][n_ids]: the checksum of each routed unit as the
+ * engine read it (0: no entry; the checksum of the deterministic replay). races[5] (may be null): host writes into a
+ * block a pending copy reads or writes, host reads of a block a pending copy writes, moves of one wave on a common
+ * slot, engine reads of a slot a pending copy writes, copies enqueued on a block whose read has not ended. Decisions
+ * that depend on timing may differ from the deterministic replay's; the bytes may not. mutation: 0, or a planted
+ * ordering fault of the cache (1: an entry published before its bytes, 2: a demand that does not wait for the prefetch
+ * bringing its unit) that the reads and the checks must catch. */
+SS_API ss_status tsb_test_dg_async_replay(const tsb_dg_replay_config* cfg, const int32_t* ids, const int32_t* preds,
+                                          const uint8_t* src_units, uint32_t seed, uint32_t delay_us, int32_t mutation,
+                                          uint64_t* read_sum, uint64_t* races);
+
 /* The device-gated context's slot table as the device holds it (cap >= the gated units; between tokens). Test hook:
  * refused unless the context was opened with dg_test_hooks = 1. */
 SS_API ss_status tsb_test_dg_table(ss_ctx* c, int32_t* out, uint32_t cap);

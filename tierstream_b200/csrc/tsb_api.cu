@@ -23,6 +23,9 @@
 namespace tsb {
 void dg_replay(const tsb_dg_replay_config* c, const int32_t* ids, const int32_t* preds, int32_t* tables,
                uint64_t* stats, const uint8_t* src_units, uint64_t* read_sum);
+void dg_async_replay(const tsb_dg_replay_config* c, const int32_t* ids, const int32_t* preds,
+                     const uint8_t* src_units, uint32_t seed, uint32_t delay_us, int32_t mutation, uint64_t* read_sum,
+                     uint64_t* races);
 const char* set_error(const std::string& msg);
 }  // namespace tsb
 
@@ -144,6 +147,12 @@ ss_status tsb_xxh64_units(const void* const* spans, const uint64_t* span_bytes, 
 ss_status tsb_test_dg_replay(const tsb_dg_replay_config* cfg, const int32_t* ids, const int32_t* preds,
                              int32_t* tables, uint64_t* stats, const uint8_t* src_units, uint64_t* read_sum) {
   return run([&] { tsb::dg_replay(cfg, ids, preds, tables, stats, src_units, read_sum); });
+}
+
+ss_status tsb_test_dg_async_replay(const tsb_dg_replay_config* cfg, const int32_t* ids, const int32_t* preds,
+                                   const uint8_t* src_units, uint32_t seed, uint32_t delay_us, int32_t mutation,
+                                   uint64_t* read_sum, uint64_t* races) {
+  return run([&] { tsb::dg_async_replay(cfg, ids, preds, src_units, seed, delay_us, mutation, read_sum, races); });
 }
 
 ss_status tsb_test_file_read(const char* path, uint64_t offset, uint64_t bytes, void* dst, uint64_t piece,
