@@ -159,6 +159,18 @@ SS_API ss_status tsb_test_file_read(const char* path, uint64_t offset, uint64_t 
 SS_API ss_status tsb_test_async_reads(const char* path, const uint64_t* offsets, uint32_t n, uint64_t bytes, void* dst,
                                       uint32_t threads, int reverse);
 
+/* Test hook: host read-ahead (the host forward mode's readahead_units) on the host alone. Unit u is unit_bytes at
+ * offsets[u] of the file at `path` (a read past its end fails with SS_E_IO); `buffers` buffers, `threads` reader
+ * threads, each read read_delay_us late. script[n_ops][3] = (op, unit, arg): op 0 requests the unit; op 1 is its
+ * fetch: the claim, then, when the claim returns the read, its end and a copy out of the buffer that ends well (arg
+ * 0), fails before it started (1) or after (2, the buffer is never reused); op 2 ends the forward; op 3 sleeps arg us.
+ * Per fetch: sums[i] = the checksum of the buffer it copied from (0: none), codes[i] = 1 (from the buffer), 0 (the
+ * file is read instead) or -status (the read failed after the claim). Per forward end: stats[7] = requested, read,
+ * landed, unused, failed, fallbacks so far, bytes read. */
+SS_API ss_status tsb_test_read_ahead(const char* path, const uint64_t* offsets, uint32_t n_units, uint64_t unit_bytes,
+                                     uint32_t buffers, uint32_t threads, uint32_t read_delay_us, const int32_t* script,
+                                     uint32_t n_ops, uint64_t* sums, int32_t* codes, uint64_t* stats);
+
 /* Test hook: the open's fill pipeline on the host alone. Unit i is `unit_bytes` at offsets[i] of the file at `path`;
  * targets[i] >= 0 lands it in slot targets[i] of `device` (a host area standing in for the arena, slots of unit_bytes
  * rounded up to 4 KiB) through a ring of `buffers` buffers of `buffer_bytes`, copied by a copy engine of its own

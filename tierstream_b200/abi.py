@@ -248,6 +248,8 @@ _PROTOS = {
     "tsb_test_dg_layout": (C.c_int, [vp, vp, P(ss_options), P(u64), u32, vp, u32]),
     "tsb_test_async_reads": (C.c_int, [C.c_char_p, P(u64), u32, u64, vp, u32, C.c_int]),
     "tsb_test_dg_async_replay": (C.c_int, [C.c_void_p, vp, vp, vp, u32, u32, C.c_int32, P(u64), P(u64)]),
+    "tsb_test_read_ahead": (C.c_int, [C.c_char_p, P(u64), u32, u64, u32, u32, u32, P(C.c_int32), u32, P(u64),
+                                      P(C.c_int32), P(u64)]),
     "tsb_test_load": (C.c_int, [C.c_char_p, P(u64), P(C.c_int32), u32, u64, vp, vp, u32, u64, u32, C.c_int, u32,
                                 C.c_int32, P(u64)]),
     "tsb_test_resident_replay": (C.c_int, [C.c_int32, C.c_int32, C.c_int32, u32, vp, vp, u32, u32, vp, u32, vp, vp,

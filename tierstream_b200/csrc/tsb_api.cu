@@ -16,6 +16,7 @@
 #include "errors.hpp"
 #include "kernels.hpp"
 #include "loader.hpp"
+#include "read_ahead.hpp"
 #include "source_file.hpp"
 #include "tierstream/tsb.h"
 #include "xxh64.hpp"
@@ -189,6 +190,68 @@ ss_status tsb_test_async_reads(const char* path, const uint64_t* offsets, uint32
       }
     }
     if (first) std::rethrow_exception(first);
+  });
+}
+
+ss_status tsb_test_read_ahead(const char* path, const uint64_t* offsets, uint32_t n_units, uint64_t unit_bytes,
+                              uint32_t buffers, uint32_t threads, uint32_t read_delay_us, const int32_t* script,
+                              uint32_t n_ops, uint64_t* sums, int32_t* codes, uint64_t* stats) {
+  return run([&] {
+    tsb::require(path && (offsets || !n_units) && (script || !n_ops) && unit_bytes >= 1 && buffers <= 64 &&
+                     threads >= 1 && threads <= 64,
+                 SS_E_INVALID, "tsb_test_read_ahead: bad argument");
+    tsb::SourceFile f(path, 4096, false);
+    const uint64_t stride = (unit_bytes + 4095) / 4096 * 4096;
+    std::vector<char*> bufs;
+    struct Free {
+      std::vector<char*>* b;
+      ~Free() {
+        for (char* p : *b) std::free(p);
+      }
+    } guard{&bufs};
+    for (uint32_t i = 0; i < buffers; ++i) {
+      bufs.push_back(static_cast<char*>(std::aligned_alloc(4096, size_t(stride))));
+      tsb::require(bufs.back() != nullptr, SS_E_NOMEM, "tsb_test_read_ahead: buffer");
+    }
+    tsb::ReadAhead ra(bufs, threads, [&](int, int unit, char* dst) {
+      if (read_delay_us) std::this_thread::sleep_for(std::chrono::microseconds(read_delay_us));
+      tsb::require(unit >= 0 && uint32_t(unit) < n_units, SS_E_INVALID, "tsb_test_read_ahead: unit");
+      f.read(dst, offsets[unit], unit_bytes);
+      return unit_bytes;
+    });
+    uint32_t claims = 0, ends = 0;
+    for (uint32_t i = 0; i < n_ops; ++i) {
+      const int32_t op = script[3 * i], unit = script[3 * i + 1], arg = script[3 * i + 2];
+      if (op == 0) {
+        ra.request(0, unit);
+      } else if (op == 1) {  // a fetch: its claim, the read's end, its copy (arg 0 ends well, 1 fails before, 2 after)
+        uint64_t s = 0;
+        int32_t code = 0;
+        if (auto e = ra.claim(0, unit)) {
+          ss_status st = SS_OK;
+          std::string msg;
+          if (const char* b = ra.wait(*e, &st, &msg)) {
+            for (uint64_t k = 0; k < unit_bytes; ++k) s += uint64_t(uint8_t(b[k])) * (k % 251 + 1);
+            code = 1;
+            ra.done(*e, arg == 0, arg == 2);
+          } else {
+            code = -int32_t(st);
+          }
+        }
+        if (sums) sums[claims] = s;
+        if (codes) codes[claims] = code;
+        ++claims;
+      } else if (op == 2) {
+        const tsb::RaStats f = ra.end_forward();
+        const uint64_t v[7] = {f.requested, f.read, f.landed, f.unused, f.failed, ra.totals().fallback, f.bytes};
+        if (stats) std::memcpy(stats + 7 * size_t(ends), v, sizeof v);
+        ++ends;
+      } else if (op == 3) {
+        std::this_thread::sleep_for(std::chrono::microseconds(std::max(0, arg)));
+      } else {
+        tsb::fail(SS_E_INVALID, "tsb_test_read_ahead: unknown op");
+      }
+    }
   });
 }
 
