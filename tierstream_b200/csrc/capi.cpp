@@ -396,16 +396,15 @@ ss_status ss_prefetch_layer(ss_ctx* c, int layer) {
     h.prefetch(layer, nullptr, -1, false);  // n < 0: every unit of the layer
   });
 }
-// Host read-ahead buffers are not in this build (readahead_units must be 0 at open), where the reference's
-// ss_host_prefetch is a no-op too (stream_ctx.cpp:1442).
-ss_status ss_host_prefetch(ss_ctx* c, int, const int32_t* ids, int n) {
+// Host read-ahead requests (stream_ctx.cpp:1441-1449): a no-op for a context without read-ahead buffers.
+ss_status ss_host_prefetch(ss_ctx* c, int layer, const int32_t* ids, int n) {
   return ctx_guard(c, [&] {
     need(n >= 0 && (ids || n == 0), "ss_host_prefetch: bad ids");
-    (void)host_of(c, "ss_host_prefetch");
+    host_of(c, "ss_host_prefetch").host_prefetch(layer, ids, n);
   });
 }
-ss_status ss_host_prefetch_layer(ss_ctx* c, int) {
-  return ctx_guard(c, [&] { (void)host_of(c, "ss_host_prefetch_layer"); });
+ss_status ss_host_prefetch_layer(ss_ctx* c, int layer) {
+  return ctx_guard(c, [&] { host_of(c, "ss_host_prefetch_layer").host_prefetch(layer, nullptr, -1); });
 }
 ss_status ss_acquire(ss_ctx* c, int layer, void* s, ss_layer_view* out) {
   return ctx_guard(c, [&] {

@@ -112,6 +112,8 @@ class HostContext {
   // ss_prefetch / ss_prefetch_layer: issue the copies of a layer's units ahead of its routes (certain: admitted as a
   // demand; speculative: the stream ring only, budgeted); allowed between forwards (they belong to the next one)
   virtual void prefetch(int layer, const int32_t* ids, int n, bool speculative) = 0;
+  // ss_host_prefetch / ss_host_prefetch_layer (n < 0): read-ahead requests (a no-op without read-ahead buffers)
+  virtual void host_prefetch(int layer, const int32_t* ids, int n) = 0;
   virtual void acquire(int layer, void* stream, bool wait_all, ss_layer_view* out) = 0;
   virtual void group_wait(int layer, int group, void* stream) = 0;
   virtual void release(int layer, void* stream) = 0;

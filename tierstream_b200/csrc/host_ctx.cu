@@ -34,6 +34,7 @@
 #include "errors.hpp"
 #include "kernels.hpp"
 #include "pinned.hpp"
+#include "read_ahead.hpp"
 #include "resident_set.hpp"
 #include "source_file.hpp"
 #include "xxh64.hpp"
@@ -64,6 +65,7 @@ struct Job {
   cudaEvent_t dst_wb_ev = nullptr;    // exclusive: the write-back of the victim whose slot it lands in
   cudaEvent_t done_ev = nullptr;   // recorded on the copy stream after the copy
   bool spec = false;               // a speculative prefetch's read, behind every demand read
+  ReadAhead::EntryPtr ra;          // host read-ahead: the unit's bytes come from this read's buffer
   std::atomic<int> state{Queued};
   ss_status err_status = SS_OK;
   std::string err;
@@ -195,6 +197,34 @@ class HostCtx final : public HostContext {
 
   // stream_ctx.cpp:1401-1440 there: certain prefetches are admitted as demands (ring when no slot), speculative ones
   // take the stream ring only, at most lookahead_budget per call, and stop at a full ring; a later route claims them.
+  // ss_host_prefetch / ss_host_prefetch_layer (n < 0: every unit): read these file-backed units into read-ahead
+  // buffers ahead of their fetch (stream_ctx.cpp:1441-1449); a no-op without read-ahead buffers. Allowed between
+  // forwards: the requests belong to the next forward.
+  void host_prefetch(int layer, const int32_t* ids, int n) override {
+    check_layer(layer, "host_prefetch");
+    require(n < 0 || ids || n == 0, SS_E_INVALID, "host_prefetch: bad ids");
+    if (!ra_) return;
+    open_forward();
+    require(L_[size_t(layer)].rs != nullptr, SS_E_INVALID, "host_prefetch: layer has no units");
+    if (n < 0)
+      for (int u = 0; u < d_.layers[size_t(layer)].n_units; ++u) ra_request(layer, u, false);
+    else
+      for (int i = 0; i < n; ++i) ra_request(layer, ids[i], false);
+  }
+  // A unit the read-ahead may read (stream_ctx.cpp:850-865): streamable, without a pinned copy, not resident, no fetch
+  // of it this forward (or one waiting for a ring slot, pending_ok), at most a buffer's bytes; once per forward.
+  void ra_request(int layer, int unit, bool pending_ok) {
+    if (!ra_) return;
+    const Lay& s = L_[size_t(layer)];
+    const Layer& l = d_.layers[size_t(layer)];
+    if (!s.rs || !l.streamable || unit < 0 || unit >= l.n_units) return;
+    const int64_t g = gidx(layer, unit);
+    if (plan_.tier[size_t(g)] == SS_TIER_PAIR || pinned_of_[size_t(g)] || s.rs->slot(unit) >= 0) return;
+    if (host_stride(l.unit_bytes) > ra_bytes_ || s.job[size_t(unit)]) return;
+    if (s.loc[size_t(unit)] != kNone && !(pending_ok && s.loc[size_t(unit)] == kRing)) return;
+    ra_->request(layer, unit);
+  }
+
   void prefetch(int layer, const int32_t* ids, int n, bool speculative) override {
     check_layer(layer, "prefetch");
     const Layer& l = d_.layers[size_t(layer)];
@@ -228,6 +258,7 @@ class HostCtx final : public HostContext {
         if (speculative) break;  // ring full: speculation never waits
         s.pending.push_back(u);
         s.loc[size_t(u)] = kRing;  // placed when a ring slot frees
+        ra_request(layer, u, true);
       }
       busy[size_t(u)] = 1;
       if (speculative) {
@@ -351,6 +382,16 @@ class HostCtx final : public HostContext {
         err = j->err;
       }
     }
+    if (ra_) {  // every fetch ended: the forward's read-ahead ends, each request counted once
+      const RaStats f = ra_->end_forward();
+      ra_st_.requested += f.requested;
+      ra_st_.read += f.read;
+      ra_st_.landed += f.landed;
+      ra_st_.unused += f.unused;
+      ra_st_.failed += f.failed;
+      ra_st_.bytes += f.bytes;
+      ra_st_.fallback = ra_->totals().fallback;
+    }
     for (size_t L = 0; L < L_.size(); ++L) {
       Lay& s = L_[L];
       if (!s.rs) continue;
@@ -473,7 +514,21 @@ class HostCtx final : public HostContext {
                   (unsigned long long)xst_.promoted, (unsigned long long)xst_.free_blocks,
                   (unsigned long long)xst_.min_free_blocks, (unsigned long long)xst_.rereads,
                   (unsigned long long)xst_.discards);
-    return buf;
+    std::string js = buf;
+    if (ra_) {  // (readahead_units = 0: the JSON stays as it was, as the reference's does)
+      char r[512];
+      std::snprintf(r, sizeof r,
+                    ",\"readahead\":{\"buffers\":%llu,\"buffer_bytes\":%llu,\"requested\":%llu,\"read\":%llu,"
+                    "\"landed\":%llu,\"unused\":%llu,\"failed\":%llu,\"fallback\":%llu,\"bytes\":%llu}}",
+                    (unsigned long long)ra_bufs_.size(), (unsigned long long)ra_bytes_,
+                    (unsigned long long)ra_st_.requested, (unsigned long long)ra_st_.read,
+                    (unsigned long long)ra_st_.landed, (unsigned long long)ra_st_.unused,
+                    (unsigned long long)ra_st_.failed, (unsigned long long)ra_->totals().fallback,
+                    (unsigned long long)ra_st_.bytes);
+      js.pop_back();  // the closing brace
+      js += r;
+    }
+    return js;
   }
 
   void test_locs(int layer, int32_t* out, int n) const override {
@@ -593,6 +648,7 @@ class HostCtx final : public HostContext {
       batch_.push_back(j);
       return;
     }
+    if (ra_ && !j->spec) j->ra = ra_->claim(j->layer, j->unit);  // a speculative read takes the ordinary path
     {
       std::lock_guard<std::mutex> lk(q_mu_);
       (j->spec ? spec_queue_ : queue_).push_back(j);
@@ -685,6 +741,10 @@ class HostCtx final : public HostContext {
         j = q.front();
         q.pop_front();
       }
+      if (j->ra) {  // its bytes are in a read-ahead buffer (or will be once that read ends)
+        land_read_ahead(*j);
+        continue;
+      }
       size_t buf = 0;
       {
         std::unique_lock<std::mutex> lk(st_mu_);
@@ -729,6 +789,44 @@ class HostCtx final : public HostContext {
       }
       done_cv_.notify_all();
     }
+  }
+  // A fetch whose unit the read-ahead reads: its copy comes out of that buffer once the read ended; the buffer comes
+  // back after the copy (a copy that failed after it started keeps it out of use); a failed read fails the fetch.
+  void land_read_ahead(Job& j) {
+    const Layer& l = d_.layers[size_t(j.layer)];
+    bool issued = false;
+    try {
+      ss_status st = SS_OK;
+      std::string msg;
+      const char* src = ra_->wait(*j.ra, &st, &msg);
+      if (!src) fail(st, msg);
+      {
+        std::lock_guard<std::mutex> lk(copy_mu_);
+        if (j.wait_ev) ck(cudaStreamWaitEvent(copy_, j.wait_ev, 0), "cudaStreamWaitEvent (slot reuse)");
+        if (j.dst_wb_ev) ck(cudaStreamWaitEvent(copy_, j.dst_wb_ev, 0), "cudaStreamWaitEvent (victim written back)");
+        issued = true;
+        ck(cudaMemcpyAsync(j.dst, src, size_t(l.unit_bytes), cudaMemcpyHostToDevice, copy_),
+           "cudaMemcpyAsync (read-ahead)");
+        ck(cudaEventRecord(j.done_ev, copy_), "cudaEventRecord (read-ahead)");
+      }
+      ck(cudaEventSynchronize(j.done_ev), "cudaEventSynchronize (read-ahead buffer reuse)");
+      ra_->done(*j.ra, true, true);
+      j.state.store(Job::Done);
+    } catch (const Error& e) {
+      ra_->done(*j.ra, false, issued);
+      j.err_status = e.status();
+      j.err = e.what();
+      j.state.store(Job::Failed);
+    } catch (const std::exception& e) {
+      ra_->done(*j.ra, false, issued);
+      j.err_status = SS_E_BACKEND;
+      j.err = e.what();
+      j.state.store(Job::Failed);
+    }
+    {
+      std::lock_guard<std::mutex> lk(q_mu_);
+    }
+    done_cv_.notify_all();
   }
   void wait_quiet(Job& j) {
     std::unique_lock<std::mutex> lk(q_mu_);
@@ -931,6 +1029,7 @@ class HostCtx final : public HostContext {
       if (!fetch_into_ring(layer, u)) {
         s.pending.push_back(u);
         s.loc[size_t(u)] = kRing;  // placed when a ring slot frees
+        ra_request(layer, u, true);
       }
     flush_copies();
     st.admitted += a.admitted.size();
@@ -946,7 +1045,7 @@ class HostCtx final : public HostContext {
     require(!(excl_ && !o_.fill_residents), SS_E_INVALID, "open: the exclusive tier mode needs fill_residents = 1");
     require(!(excl_ && o_.exclusive_discard && d_.tiers == Tiers::Pinned), SS_E_INVALID,
             "open: exclusive_discard needs a descriptor whose tiers allow disk (tiers = \"pinned\" refuses it)");
-    require(o_.readahead_units == 0, SS_E_UNSUPPORTED, "open: host read-ahead is not in this build");
+    require(o_.readahead_units <= 64, SS_E_INVALID, "open: readahead_units must be <= 64");
     require(!o_.spec_persistent, SS_E_UNSUPPORTED,
             "open: spec_persistent is not in this build (speculative prefetches take the stream ring)");
     ck(cudaSetDevice(o_.device), "cudaSetDevice");
@@ -1030,6 +1129,35 @@ class HostCtx final : public HostContext {
       ck(cudaHostAlloc(&p, size_t(disk_unit), cudaHostAllocPortable), "cudaHostAlloc (staging)");
       staging_.push_back(static_cast<char*>(p));
       st_free_.push_back(i);
+    }
+    // host read-ahead: readahead_units pinned buffers of the largest streamable unit that has no pinned copy (none
+    // when every such unit is pinned or a pair's), read by reader threads of their own
+    if (o_.readahead_units) {
+      for (size_t L = 0; L < d_.layers.size(); ++L) {
+        if (!d_.layers[L].streamable) continue;
+        for (int u = 0; u < d_.layers[L].n_units; ++u) {
+          const uint8_t t = plan_.tier[size_t(gidx(int(L), u))];
+          if (t == SS_TIER_PINNED || t == SS_TIER_PAIR) continue;
+          ra_bytes_ = std::max(ra_bytes_, host_stride(d_.layers[L].unit_bytes));
+          break;
+        }
+      }
+      if (ra_bytes_) {
+        for (uint32_t i = 0; i < o_.readahead_units; ++i) {
+          void* p = nullptr;
+          ck(cudaHostAlloc(&p, size_t(ra_bytes_), cudaHostAllocPortable), "cudaHostAlloc (read-ahead)");
+          ra_bufs_.push_back(static_cast<char*>(p));
+        }
+        ra_ = std::make_unique<ReadAhead>(ra_bufs_, o_.reader_threads, [this](int layer, int unit, char* dst) {
+          const Layer& l = d_.layers[size_t(layer)];
+          read_unit(layer, unit, dst);
+          if (o_.verify_hash && !l.hash.empty())
+            require(xxh64(dst, size_t(l.unit_bytes)) == l.hash[size_t(unit)], SS_E_HASH,
+                    "read: unit (" + std::to_string(layer) + ", " + std::to_string(unit) +
+                        ") differs from its descriptor hash");
+          return l.unit_bytes;
+        });
+      }
     }
     // layers: pools, events, tables
     L_.resize(d_.layers.size());
@@ -1155,6 +1283,7 @@ class HostCtx final : public HostContext {
     for (auto& t : workers_)
       if (t.joinable()) t.join();
     workers_.clear();
+    ra_.reset();  // its readers end before their buffers go
     if (copy_) cudaStreamSynchronize(copy_);
     if (wb_stream_) cudaStreamSynchronize(wb_stream_);
     cudaDeviceSynchronize();
@@ -1181,6 +1310,8 @@ class HostCtx final : public HostContext {
     blocks_ev_ = wb_mark_ev_ = nullptr;
     for (char* s : staging_) cudaFreeHost(s);
     staging_.clear();
+    for (char* s : ra_bufs_) cudaFreeHost(s);
+    ra_bufs_.clear();
     for (cudaEvent_t e : all_ev_) cudaEventDestroy(e);
     all_ev_.clear();
     if (copy_) cudaStreamDestroy(copy_);
@@ -1202,6 +1333,10 @@ class HostCtx final : public HostContext {
   std::vector<const char*> pinned_of_;
   std::vector<char*> staging_;
   std::vector<size_t> st_free_;
+  std::unique_ptr<ReadAhead> ra_;  // host read-ahead (readahead_units > 0 and a unit without a pinned copy)
+  std::vector<char*> ra_bufs_;
+  uint64_t ra_bytes_ = 0;
+  RaStats ra_st_;
   std::mutex st_mu_;
   std::condition_variable st_cv_;
   cudaStream_t copy_ = nullptr;

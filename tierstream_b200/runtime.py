@@ -194,6 +194,15 @@ class HostContext:
     def prefetch_layer(self, layer):
         abi.check(abi.load().ss_prefetch_layer(self.h, layer))
 
+    def host_prefetch_layer(self, layer):
+        """Read-ahead requests for every unit of the layer (ss_host_prefetch_layer)."""
+        abi.check(abi.load().ss_host_prefetch_layer(self.h, layer))
+
+    def stats_json(self):
+        p, n = C.c_void_p(), C.c_size_t()
+        abi.check(abi.load().ss_stats_to_json(self.h, C.byref(p), C.byref(n)))
+        return abi.take_text(p, n.value)
+
     def acquire(self, layer, stream):
         v = abi.ss_layer_view()
         abi.check(abi.load().ss_acquire(self.h, layer, stream, C.byref(v)))
