@@ -2,7 +2,6 @@
 source bytes (the oracle's checksum of the model file), the slot table after every token equals the reference
 DgCore's on the same trace (deterministic schedule), and the failure paths end the token with an error instead of a
 hang."""
-import json
 import os
 
 import numpy as np
@@ -71,30 +70,6 @@ def test_bytes_and_tables_match_reference(small_model, orc, ref, monkeypatch, co
         for L in range(m.layers):
             for u in range(m.units):
                 run.ctx.check_unit(L, u)
-    finally:
-        run.close()
-
-
-@pytest.mark.parametrize("load", [{"TSB_LOAD_SERIAL": "1"},
-                                  {"TSB_LOAD_BUFFERS": "1", "TSB_LOAD_BUFFER_MIB": "1", "TSB_LOAD_READERS": "3"},
-                                  {"TSB_LOAD_BUFFERS": "3", "TSB_LOAD_READERS": "16"}, {}])
-def test_open_fill_lands_every_unit(small_model, orc, monkeypatch, load):
-    """The open's fill, phased or pipelined with rings of one buffer of a few units up to the default: every resident's
-    slot and every pinned unit's block equals the source, and the tokens read the right bytes."""
-    for k, v in load.items():
-        monkeypatch.setenv(k, v)
-    m = small_model
-    run = harness.DgRun(m, residents_per_layer=5, max_ids=2, verify=True)
-    try:
-        for L in range(m.layers):
-            for u in range(m.units):
-                run.ctx.check_unit(L, u)
-        o = json.loads(run.ctx.stats_json())["open"]
-        assert o["load"] == ("serial" if load.get("TSB_LOAD_SERIAL") else "pipeline")
-        if o["load"] == "pipeline":
-            assert o["load_slot_units"] == 5 * m.layers and o["load_pinned_units"] == (m.units - 5) * m.layers
-            assert 1 <= o["load_buffers"] <= int(load.get("TSB_LOAD_BUFFERS", 4))
-        run_tokens(run, synth.zipf_trace(10, m.layers, m.units, 2, s=0.8, seed=21), expected_sums(m, orc))
     finally:
         run.close()
 

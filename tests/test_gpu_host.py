@@ -313,64 +313,3 @@ def test_layer_prefetch_overlaps_the_blob_stream(orc, ref):
     finally:
         ctx.close()
 
-
-@pytest.mark.parametrize("ra", [0, 3])
-def test_host_read_ahead_lands_file_blobs(orc, ra):
-    """C3-shaped, scaled, with the streamed blobs in the model file only (tier DISK): ss_host_prefetch_layer for the
-    next two layers ahead of each layer's ss_layer_all. With readahead_units = 3 the blobs are read into the read-ahead
-    buffers and land from there; every blob read through the table has its bytes, with and without read-ahead, and
-    the read-ahead counters add up (landed + unused = read <= requested)."""
-    import json
-    m = synth.Model(os.path.join(harness.model_dir(), "tsb-test-blobs.bin"), layers=12, units=1,
-                    part_bytes=((1 << 20) + 17,), seed=5, top_k=1)
-    m.write()
-    d = json.loads(m.desc(order="prefix", tiers="pinned|disk"))
-    for lay in d["layers"]:
-        lay["kind"] = "blob"
-        lay.pop("top_k")
-    desc_json = json.dumps(d)
-    tiers = [abi.SS_TIER_RESIDENT] * 5 + [abi.SS_TIER_DISK] * 7
-    b = abi.budget_defaults()
-    b.device_bytes = 1 << 30
-    b.margin_gib = 1.0 / 1024
-    b.margin_fraction = 0.0
-    b.ring_slots = 2
-    b.host_pinned_bytes = 1 << 30
-    o = abi.options_defaults()
-    o.forward_mode = abi.SS_FORWARD_HOST
-    o.verify_hash = 1
-    o.readahead_units = ra
-    desc = runtime.Desc(desc_json)
-    plan = runtime.Plan(desc, b, tiers=tiers)
-    ctx = runtime.HostContext(desc, plan, o)
-    eng = abi.load_engine()
-    want = expected(m, orc)
-    s = torch.cuda.Stream()
-    ids_dev = torch.zeros(1, dtype=torch.int32, device="cuda")
-    out = torch.zeros(1, dtype=torch.int64, device="cuda")
-    try:
-        for f in range(3):
-            ctx.begin()
-            for L in range(m.layers):
-                for k in (1, 2):
-                    if L + k < m.layers:
-                        ctx.host_prefetch_layer(L + k)
-                ctx.layer_all(L)
-                v = ctx.acquire(L, s.cuda_stream)
-                with torch.cuda.stream(s):
-                    assert eng.tse_read_table(C_ptr(v.table_dev), ids_dev.data_ptr(), 1, m.unit_bytes, out.data_ptr(),
-                                              8, s.cuda_stream) == 0
-                s.synchronize()
-                assert int(out[0].item()) == int(want[L]), "forward %d layer %d read wrong bytes" % (f, L)
-                ctx.check_unit(L, 0)
-                ctx.release(L, s.cuda_stream)
-            ctx.end()
-        st = json.loads(ctx.stats_json())
-        if ra:
-            r = st["readahead"]
-            assert r["buffers"] == ra and r["landed"] > 0 and r["failed"] == 0
-            assert r["landed"] + r["unused"] == r["read"] <= r["requested"]
-        else:
-            assert "readahead" not in st
-    finally:
-        ctx.close()
