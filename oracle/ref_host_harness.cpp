@@ -219,8 +219,9 @@ extern "C" __attribute__((visibility("default"))) int oref_dg_layout(const char*
 }
 
 // The reference's own descriptor parser and planner through its C ABI (capi.cpp): the descriptor (status, its JSON, every
-// layer's units and unit bytes), then a plan made from a budget and benefits (mode 0, ss_plan_make) or given tiers (mode
-// 1, ss_plan_from_tiers): every unit's tier, the totals and the plan's JSON. Returns the plan's status (or the
+// layer's units and unit bytes), then a plan made from a budget and benefits (mode 0, ss_plan_make), given tiers (mode
+// 1, ss_plan_from_tiers) or a plan JSON passed as the tiers' bytes (mode 2, ss_plan_from_json): every unit's tier, the
+// totals and the plan's JSON. Returns the plan's status (or the
 // descriptor's when that failed, with *desc_status set).
 extern "C" __attribute__((visibility("default"))) int oref_plan(
     const char* desc_json, size_t len, const ss_budget* budget, const double* benefit, size_t n_benefit,
@@ -245,8 +246,10 @@ extern "C" __attribute__((visibility("default"))) int oref_plan(
     layer_out[2 * l + 1] = ss_desc_unit_bytes(d, l);
   }
   ss_plan* p = nullptr;
-  const ss_status st = mode == 0 ? ss_plan_make(d, budget, benefit, n_benefit, &p)
-                                 : ss_plan_from_tiers(d, budget, tiers, n_tiers, &p);
+  const ss_status st =
+      mode == 0   ? ss_plan_make(d, budget, benefit, n_benefit, &p)
+      : mode == 1 ? ss_plan_from_tiers(d, budget, tiers, n_tiers, &p)
+                  : ss_plan_from_json(d, budget, reinterpret_cast<const char*>(tiers), n_tiers, &p);  // (tiers: JSON)
   if (st != SS_OK) {
     if (err && errlen) std::snprintf(err, errlen, "%s", ss_last_error());
     ss_desc_free(d);

@@ -1,8 +1,9 @@
 """The descriptor parser and the planner against the reference's own (its capi.cpp, desc.cpp and plan.cpp compiled
 from its sources) on the CPU: random desc-v1 descriptors (every layer kind, parts, sources, orders, tier sets, hashes,
 benefits, fixed bytes, broken ones too) and budgets, through the same C ABI calls. The descriptor's status, its JSON
-and every layer's units and unit bytes are equal; ss_plan_make (budget and benefits) and ss_plan_from_tiers (given
-tiers) give the same status, the same tier for every unit, the same totals and the same plan JSON."""
+and every layer's units and unit bytes are equal; ss_plan_make (budget and benefits), ss_plan_from_tiers (given
+tiers) and ss_plan_from_json (a plan JSON of tier letters, broken now and then) give the same status, the same tier
+for every unit, the same totals and the same plan JSON."""
 import ctypes as C
 import json
 
@@ -95,6 +96,8 @@ def ours(text, b, benefit, tiers, mode):
     if mode == 0:
         bb = (C.c_double * max(1, len(benefit)))(*benefit) if benefit is not None else None
         st = lib.ss_plan_make(h, C.byref(b), bb, len(benefit) if benefit is not None else 0, C.byref(plan))
+    elif mode == 2:
+        st = lib.ss_plan_from_json(h, C.byref(b), bytes(tiers), len(tiers), C.byref(plan))
     else:
         t = (C.c_uint8 * max(1, len(tiers)))(*tiers)
         st = lib.ss_plan_from_tiers(h, C.byref(b), t, len(tiers), C.byref(plan))
@@ -122,7 +125,8 @@ def reference(text, b, benefit, tiers, mode):
     dst = C.c_int()
     err = C.create_string_buffer(512)
     bb = np.asarray(benefit if benefit is not None else [0.0], dtype=np.float64)
-    tt = np.asarray(tiers if tiers else [0], dtype=np.uint8)
+    tt = np.frombuffer(bytes(tiers), dtype=np.uint8) if mode == 2 and tiers else \
+        np.asarray(tiers if tiers else [0], dtype=np.uint8)
     st = oracle.ref().oref_plan(raw, len(raw), C.byref(b), bb.ctypes.data if benefit is not None else None,
                                 len(benefit) if benefit is not None else 0, tt.ctypes.data, len(tiers), mode,
                                 tiers_out.ctypes.data, cap, C.byref(tot), js, len(js), ds, len(ds), lay.ctypes.data,
@@ -140,6 +144,26 @@ def reference(text, b, benefit, tiers, mode):
     return out
 
 
+def plan_json(r, d):
+    """A plan JSON for ss_plan_from_json: per layer one letter per unit (R P D X B); one in six broken (a wrong
+    length, a bad letter, a missing layer, no "tiers")."""
+    per = [L.get("n_units", 1 if L["kind"] == "blob" else 0) for L in d["layers"]]
+    layers = ["".join(r.choice(list("RPPDB"), size=n)) for n in per]
+    if r.random() < 1 / 6:
+        what = int(r.integers(0, 4))
+        if what == 0 and any(per):
+            i = next(k for k, n in enumerate(per) if n)
+            layers[i] = layers[i][:-1]
+        elif what == 1 and any(per):
+            i = next(k for k, n in enumerate(per) if n)
+            layers[i] = "Q" + layers[i][1:]
+        elif what == 2:
+            layers = layers[:-1]
+        else:
+            return json.dumps({"plan": layers})
+    return json.dumps({"tiers": layers})
+
+
 @pytest.mark.parametrize("seed", range(200))
 def test_descriptor_and_plan_match_reference(ref, seed):
     r = np.random.default_rng(80_000 + seed)
@@ -147,9 +171,11 @@ def test_descriptor_and_plan_match_reference(ref, seed):
     text = json.dumps(d)
     b = random_budget(r, d)
     total = sum(L.get("n_units", 1 if L["kind"] == "blob" else 0) for L in d["layers"])
-    mode = int(r.integers(0, 2))
+    mode = int(r.integers(0, 3))
     benefit = [float(x) for x in r.uniform(0, 3, size=total)] if (mode == 0 and r.random() < 0.5) else None
     tiers = [int(x) for x in r.choice([0, 1, 1, 2], size=total)] if mode == 1 else []
+    if mode == 2:
+        tiers = plan_json(r, d).encode()
     a, e = ours(text, b, benefit, tiers, mode), reference(text, b, benefit, tiers, mode)
     assert a["desc_status"] == e["desc_status"], (a, e)
     if a["desc_status"]:
