@@ -57,6 +57,8 @@ def ref():
         lib.oref_resident_replay.argtypes = [C.c_int32, C.c_int32, C.c_int32, C.c_uint32, C.c_void_p, C.c_void_p,
                                              C.c_uint32, C.c_uint32, C.c_void_p, C.c_uint32, C.c_void_p, C.c_void_p,
                                              C.c_void_p, C.c_void_p, C.c_void_p, C.c_char_p, C.c_size_t]
+        lib.oref_defaults.restype = None
+        lib.oref_defaults.argtypes = [C.c_void_p, C.c_uint32, C.c_void_p, C.c_uint32]
         lib.oref_plan.restype = C.c_int
         lib.oref_plan.argtypes = [C.c_char_p, C.c_size_t, C.c_void_p, C.c_void_p, C.c_size_t, C.c_void_p, C.c_size_t,
                                   C.c_int, C.c_void_p, C.c_size_t, C.c_void_p, C.c_char_p, C.c_size_t, C.c_char_p,

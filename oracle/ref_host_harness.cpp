@@ -267,3 +267,11 @@ extern "C" __attribute__((visibility("default"))) int oref_plan(
   ss_desc_free(d);
   return SS_OK;
 }
+
+// The reference's defaults for the versioned structs (capi.cpp): ss_options_defaults_sized and
+// ss_budget_defaults_sized into caller buffers of the given sizes.
+extern "C" __attribute__((visibility("default"))) void oref_defaults(void* options, uint32_t options_size, void* budget,
+                                                                     uint32_t budget_size) {
+  ss_options_defaults_sized(static_cast<ss_options*>(options), options_size);
+  ss_budget_defaults_sized(static_cast<ss_budget*>(budget), budget_size);
+}

@@ -86,3 +86,27 @@ def test_round_defaults_and_cancel_without_a_context():
     assert (p.struct_size, p.flags, p.budget_bytes, p.max_units) == (C.sizeof(p), 0, 0, 96)
     assert abs(p.hysteresis - 1.25) < 1e-7 and abs(p.decay - 0.85) < 1e-7
     assert lib.ss_dg_round_cancel(None) == abi.SS_E_INVALID
+
+
+def test_struct_defaults_match_the_reference(ref):
+    """ss_options_defaults_sized and ss_budget_defaults_sized fill every byte as the reference's own do (its capi.cpp,
+    compiled), at the full size and at a caller's older, shorter size (the tail left as the caller had it), except one
+    field: ss_options.backend defaults to SS_BACKEND_CUDA here, the only backend this build has, where the reference
+    defaults to its CPU backend (capi.cpp:111), so that defaults open a context on this build."""
+    import ctypes as C
+    import oracle
+    from tierstream_b200 import abi
+    lib = abi.load()
+    for size_o, size_b in ((C.sizeof(abi.ss_options), C.sizeof(abi.ss_budget)), (80, 48)):
+        ours_o = (C.c_uint8 * C.sizeof(abi.ss_options))(*([0xA5] * C.sizeof(abi.ss_options)))
+        ours_b = (C.c_uint8 * C.sizeof(abi.ss_budget))(*([0xA5] * C.sizeof(abi.ss_budget)))
+        ref_o = (C.c_uint8 * C.sizeof(abi.ss_options))(*([0xA5] * C.sizeof(abi.ss_options)))
+        ref_b = (C.c_uint8 * C.sizeof(abi.ss_budget))(*([0xA5] * C.sizeof(abi.ss_budget)))
+        lib.ss_options_defaults_sized(C.cast(ours_o, C.POINTER(abi.ss_options)), size_o)
+        lib.ss_budget_defaults_sized(C.cast(ours_b, C.POINTER(abi.ss_budget)), size_b)
+        oracle.ref().oref_defaults(C.cast(ref_o, C.c_void_p), size_o, C.cast(ref_b, C.c_void_p), size_b)
+        off = abi.ss_options.backend.offset
+        assert ours_o[off] == abi.SS_BACKEND_CUDA and ref_o[off] == 0  # SS_BACKEND_CPU
+        ref_o[off] = abi.SS_BACKEND_CUDA
+        assert bytes(ours_o) == bytes(ref_o), "ss_options defaults differ at size %d" % size_o
+        assert bytes(ours_b) == bytes(ref_b), "ss_budget defaults differ at size %d" % size_b
