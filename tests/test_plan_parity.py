@@ -92,6 +92,13 @@ def ours(text, b, benefit, tiers, mode):
     abi.check(lib.ss_desc_to_json(h, C.byref(p), C.byref(n)))
     desc_json = abi.take_text(p, n.value)
     layers = [(lib.ss_desc_layer_units(h, l), lib.ss_desc_unit_bytes(h, l)) for l in range(lib.ss_desc_n_layers(h))]
+    base = 0  # every unit's global index and the total, from the layers' units
+    for l, (units, _) in enumerate(layers):
+        for u in (0, units - 1, units, -1):
+            assert lib.ss_desc_unit_index(h, l, u) == (base + u if 0 <= u < units else -1)
+        base += units
+    assert lib.ss_desc_total_units(h) == base
+    assert lib.ss_desc_unit_index(h, len(layers), 0) == -1
     plan = C.c_void_p()
     if mode == 0:
         bb = (C.c_double * max(1, len(benefit)))(*benefit) if benefit is not None else None
