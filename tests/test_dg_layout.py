@@ -1,7 +1,8 @@
 """The device-gated layout ss_open takes (slots, banks, blocks, spare and file units, staging buffers, the resolved
 read depth and score weights, the residents) against the reference's own dg_layout on the same descriptor, tiers,
 budget and options, on the CPU: every number is identical, or both refuse with the same status. Options this build
-refuses as unsupported (landings, bank keep, adaptive depth, priors, host read-ahead) are left out."""
+refuses as unsupported (landings, bank keep, adaptive depth, priors) are left out; host read-ahead, which both refuse
+with SS_E_INVALID in this mode, is tests/test_open_refusals.py's."""
 import ctypes as C
 import os
 
