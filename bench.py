@@ -28,6 +28,8 @@ import sys
 import tempfile
 import time
 
+import numpy as np
+
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
@@ -318,8 +320,11 @@ def main():
         if dist:
             dist.barrier()
 
-    model = synth.Model(model_path(), LAYERS, UNITS, [PART] * 3, seed=0, top_k=TOP_K)
     qwen = a.workload == "qwen3-235b-a22b-peer"
+    # descriptor hashes (the stores' and the landings' checks on the device) for every model written to disk; the
+    # Qwen3-shaped stores are written on the device from the generator and checked by the readers' sums instead
+    hashed = not qwen
+    model = synth.Model(model_path(), LAYERS, UNITS, [PART] * 3, seed=0, top_k=TOP_K, with_hash=hashed)
     if qwen and not a.peer:
         raise SystemExit("qwen3-235b-a22b-peer runs the peer tier only (its experts do not fit pinned RAM)")
     if rank == 0:
@@ -327,6 +332,7 @@ def main():
             model.create_sparse()
         else:
             model.write()
+            model.hashes()  # kept beside the model file for the other ranks
     barrier()
     peak = h2d_peak(torch) if rank == 0 and not a.peer else None
     read_peak = file_read_peak(model_path(), 3 * PART) if a.file else None
@@ -335,7 +341,6 @@ def main():
     t_open = time.perf_counter()
     setup = None
     if a.peer:
-        import numpy as np
         from tierstream_b200 import peer as peer_mod, runtime
         # the planner's input: this rank's routing counts over a calibration window of its own trace distribution
         cal = synth.zipf_trace(64, LAYERS, UNITS, TOP_K, s=ZIPF, seed=1001 + rank)
@@ -357,22 +362,38 @@ def main():
                 first = peer_mod.read_device(store.base, model.unit_bytes)
                 k0 = int(keys[0])
                 assert np.array_equal(first, model.unit_bytes_of(k0 // UNITS, k0 % UNITS)), "store fill differs"
-        setup = peer_mod.PeerSetup(runtime.Desc(model.desc()), counts, dist, world, rank, local, verify=False,
+        setup = peer_mod.PeerSetup(runtime.Desc(model.desc()), counts, dist, world, rank, local, verify=hashed,
                                    copy=1 if a.peer_copy == "ce" else 0,
                                    collective_device=torch.device("cuda", local) if dist else None, filler=filler)
+    # verify_hash with descriptor hashes: residents checked at the open, and every unit landed in a slot while decoding
+    # hashed on the device against its descriptor hash (the landing check)
     run = harness.DgRun(model, resident_keys=resident_keys(1 + rank), spare_per_layer=a.spare, max_ids=TOP_K,
                         diag=True, test_hooks=False, mode=1, slices=128, wb_defer=a.wb_defer, wb_stream=a.wb_stream,
+                        verify=hashed,
                         inclusive=inclusive, peer=setup.tier if setup else None,
                         disk_keys=disk_keys(a, resident_keys(1)) if a.file else (), disk_staging=a.staging,
                         disk_queue=a.disk_queue, policy={"lru": 0, "scored": 1, "scored_auto": 2}[a.policy])
     t_open = time.perf_counter() - t_open
     unit = model.unit_bytes
+    # the e2e leg's trace, and every routed unit's expected reader sums in both legs' modes, from the byte generator
+    # on the device (outside the timed regions)
+    ids2 = synth.zipf_trace(a.steps, LAYERS, UNITS, TOP_K, s=ZIPF, seed=101 + rank)
+    routed = np.unique(np.concatenate([(np.arange(LAYERS)[None, :, None] * UNITS + x).reshape(-1)
+                                       for x in (ids[a.warmup:], ids2)]))
+    t_exp = time.perf_counter()
+    want = {mode: np.zeros(LAYERS * UNITS, dtype=np.uint64) for mode in (0, 1)}
+    for mode in (0, 1):
+        want[mode][routed] = harness.expected_sums(model, routed, mode)
+    t_exp = time.perf_counter() - t_exp
     try:
         for t in range(a.warmup):
             run.step(ids[t])
+        run.graph_for(0)  # the e2e leg's graph (positional checksums), captured before any timed region
         # (1) device-timed: ids already in HBM (the whole trace resident), one D2D copy per step into the graph's
-        # input buffer, no host copy
+        # input buffer, no host copy; each step's reader sums kept on the device for the check after the region
         trace_dev = torch.from_numpy(ids[a.warmup:].reshape(a.steps, -1).copy()).cuda()
+        outs_dev = torch.zeros((a.steps, LAYERS * TOP_K), dtype=torch.int64, device="cuda")
+        run.stream.wait_stream(torch.cuda.current_stream())
         s0 = run.ctx.stats()
         f0 = json.loads(run.ctx.stats_json())
         j0 = f0["dg"]
@@ -386,6 +407,7 @@ def main():
             with torch.cuda.stream(run.stream):
                 run.ids_dev.copy_(trace_dev[t], non_blocking=True)
                 run.graph.launch()
+                outs_dev[t].copy_(run.out_dev, non_blocking=True)
             run.ctx.end()
             if a.round_every and (t + 1) % a.round_every == 0:
                 run.ctx.round()
@@ -398,23 +420,35 @@ def main():
         f1 = json.loads(run.ctx.stats_json())
         j1 = f1["dg"]
         layer_path = miss_layer_path(run.ctx, LAYERS)
+        c0, c1 = f0["check"], f1["check"]
+        check = {"on": bool(c1["on"]), "units_per_token": round((c1["units"] - c0["units"]) / a.steps, 3),
+                 "gb_per_token": round((c1["bytes"] - c0["bytes"]) / a.steps / 1e9, 3),
+                 "launches_per_token": round((c1["launches"] - c0["launches"]) / a.steps, 3),
+                 "merged_per_token": round((c1["merged"] - c0["merged"]) / a.steps, 3),
+                 "hold_waits": c1["hold_waits"] - c0["hold_waits"], "mismatches": c1["mismatches"] - c0["mismatches"],
+                 "end_wait_ms_per_token": round((c1["end_wait_s"] - c0["end_wait_s"]) * 1e3 / a.steps, 3)}
         peer_units = f1["peer"]["peer_units"] - f0["peer"]["peer_units"]
         self_units = f1["peer"]["self_units"] - f0["peer"]["self_units"]
         units_moved = (s1["fetched"] - s0["fetched"]) + (s1["prefetched"] - s0["prefetched"])
         moved = units_moved * unit
         dma_ms = j1["dma_ms_total"] - j0["dma_ms_total"]
         land_launches = j1["land_launches"] - j0["land_launches"]
-        # (2) end to end: the same steps of a second trace window through the ABI with host buffers
-        ids2 = synth.zipf_trace(a.steps, LAYERS, UNITS, TOP_K, s=ZIPF, seed=101 + rank)
+        # (2) end to end: the same steps of a second trace window through the ABI with host buffers, the readers
+        # computing the positional checksum (the reference GPU tests' check)
         s2 = run.ctx.stats()
+        outs2 = np.zeros((a.steps, LAYERS, TOP_K), dtype=np.uint64)
         barrier()
         w0 = time.perf_counter()
         for t in range(a.steps):
-            run.step(ids2[t])
+            outs2[t] = run.step(ids2[t], mode=0)
             if a.round_every and (t + 1) % a.round_every == 0:
                 run.ctx.round()
         w1 = time.perf_counter()
         barrier()
+        # every routed unit of both legs as its reader saw it, against the generator's sums
+        n1, bad1, first1 = harness.check_reads(outs_dev.cpu().numpy().view(np.uint64).reshape(a.steps, LAYERS, TOP_K),
+                                               ids[a.warmup:], UNITS, want[1])
+        n0, bad0, first0 = harness.check_reads(outs2, ids2, UNITS, want[0])
         s3 = run.ctx.stats()
         moved_e2e = ((s3["fetched"] - s2["fetched"]) + (s3["prefetched"] - s2["prefetched"])) * unit
         e2e_s = w1 - w0
@@ -436,13 +470,19 @@ def main():
             setup.close()
 
     tot = torch.tensor([moved, moved_e2e, dev_ms, e2e_s, dma_ms], dtype=torch.float64, device="cuda")
+    ver = torch.tensor([2 * a.steps, n1 + n0, bad1 + bad0], dtype=torch.int64, device="cuda")
     if dist:
         s = tot[[0, 1]].clone()
         m = tot[[2, 3, 4]].clone()
         dist.all_reduce(s, op=dist.ReduceOp.SUM)
         dist.all_reduce(m, op=dist.ReduceOp.MAX)
+        dist.all_reduce(ver, op=dist.ReduceOp.SUM)
         tot = torch.cat([s, m])
     moved_all, moved_e2e_all, dev_ms_max, e2e_s_max, dma_ms_max = [float(x) for x in tot.cpu()]
+    v_tokens, v_units, v_bad = [int(x) for x in ver.cpu()]
+    if bad1 or bad0:
+        print("rank %d: %d of %d reads differ from the generator (first: timed leg %s, e2e leg %s)" %
+              (rank, bad1 + bad0, n1 + n0, first1, first0), file=sys.stderr)
     if rank != 0:
         if dist:
             dist.destroy_process_group()
@@ -475,7 +515,18 @@ def main():
                                      "the land kernel), whose DRAM bytes ncu does not attribute to one kernel; ncu "
                                      "captures of the land kernel alone show DRAM traffic at or below its algorithmic "
                                      "bytes"},
-        "gpu_launches": int(a.steps * (2 + 2 * LAYERS) + land_launches + a.steps * LAYERS),
+        "verified": {"tokens": v_tokens, "units": v_units, "mismatches": v_bad, "ranks": world,
+                     "how": "every routed unit of every timed token (both legs, every rank) as the engine's reader "
+                            "read it through the slot table: word sums in the device-timed leg, positional checksums "
+                            "sum(byte x (pos %% 251 + 1)) in the e2e leg, against sums computed on the device from the "
+                            "byte generator alone (%.2f s, outside the timed regions)" % t_exp,
+                     "stores_checked": bool(a.peer and hashed)},
+        "gpu_launches": int(a.steps * (2 + 2 * LAYERS) + land_launches + a.steps * LAYERS +
+                            (c1["launches"] - c0["launches"])),
+        "landing_check": dict(check, how="every unit copied into a slot hashed on the device (K3, xxh64) against "
+                                          "its descriptor hash on a low-priority stream behind the layer's ready word; "
+                                          "a copy into a slot still being hashed waits for it (hold_waits); each "
+                                          "ss_end waits for the previous token's hashes (end_wait)"),
         "clocks": clk, "open_s": round(t_open, 2), "open": open_stats, "dg": dg, "miss_layer_path": layer_path,
         "options": {"wb_defer": a.wb_defer, "wb_stream": a.wb_stream, "spare_slots_per_layer": a.spare,
                     "inclusive_blocks": inclusive, "policy": a.policy, "round_every": a.round_every,
@@ -533,7 +584,7 @@ def main():
     print(json.dumps(line))
     if dist:
         dist.destroy_process_group()
-    return 0
+    return 1 if v_bad else 0
 
 
 if __name__ == "__main__":

@@ -142,6 +142,12 @@ SS_API ss_status tsb_test_dg_async_replay(const tsb_dg_replay_config* cfg, const
  * refused unless the context was opened with dg_test_hooks = 1. */
 SS_API ss_status tsb_test_dg_table(ss_ctx* c, int32_t* out, uint32_t cap);
 
+/* Test hook of the landing check: flips the byte at `offset` of the pinned block holding unit (layer, unit) of a
+ * device-gated context (the unit must be in pinned RAM, between tokens; refused without dg_test_hooks). A later miss
+ * on the unit lands the wrong byte, which the device's check of every landed unit reports at an ss_end (SS_E_HASH) and
+ * repairs from the unit's file. */
+SS_API ss_status tsb_test_dg_corrupt(ss_ctx* c, int layer, int unit, uint64_t offset);
+
 /* Host forward mode, between ss_acquire and ss_release of `layer` (test hook): per unit of the layer, out[2 u] = where
  * its table entry points (1 = its persistent slot, 2 = a stream ring slot, 0 = no entry) and out[2 u + 1] = that slot
  * (-1 for no entry). n must be the layer's units. */

@@ -60,7 +60,7 @@ def test_gpu_dg_default_setup():
 
 @pytest.mark.parametrize("with_profile", [False, True])
 def test_gpu_policies_scored_setup(with_profile):
-    """test_zzz_gpu_newest.test_scored_tables_match_reference: two spare slots and blocks per layer, SCORED, with and
+    """test_zy_gpu_newest.test_scored_tables_match_reference: two spare slots and blocks per layer, SCORED, with and
     without a profile (which the layout checks against the descriptor's identity)."""
     m = model("tsb-test-scored.bin", 13)
     prof = None
@@ -78,7 +78,7 @@ def test_gpu_policies_scored_setup(with_profile):
 
 @pytest.mark.parametrize("wb_defer", [0, 1])
 def test_gpu_policies_rounds_setup(wb_defer):
-    """test_zzz_gpu_newest.test_rounds_match_reference."""
+    """test_zy_gpu_newest.test_rounds_match_reference."""
     m = model("tsb-test-scored.bin", 13)
     s = harness.DgSetup(m, residents_per_layer=3, max_ids=2, wb_defer=wb_defer)
     out, res = layout(s)
@@ -87,7 +87,7 @@ def test_gpu_policies_rounds_setup(wb_defer):
 
 
 def test_gpu_policies_lru_setup_has_no_score_tables():
-    """test_zzz_gpu_newest.test_set_policy_needs_scoring_at_open: opened with LRU."""
+    """test_zy_gpu_newest.test_set_policy_needs_scoring_at_open: opened with LRU."""
     s = harness.DgSetup(model("tsb-test-scored.bin", 13), residents_per_layer=3, max_ids=2)
     out, _ = layout(s)
     assert int(out[SCORED]) == 0
@@ -108,7 +108,7 @@ def test_gpu_dg_file_tier_setup(S_):
 
 
 def test_gpu_dg_open_fill_setup():
-    """test_zzz_gpu_newest.test_open_fill_lands_every_unit: five residents per layer, hashes checked."""
+    """test_zy_gpu_newest.test_open_fill_lands_every_unit: five residents per layer, hashes checked."""
     m = model("tsb-test-small.bin", 3)
     s = harness.DgSetup(m, residents_per_layer=5, max_ids=2, verify=True)
     out, res = layout(s)
@@ -117,7 +117,7 @@ def test_gpu_dg_open_fill_setup():
 
 @pytest.mark.parametrize("with_profile", [False, True])
 def test_gpu_policies_scored_trace_scores(ref, with_profile):
-    """test_zzz_gpu_newest.test_scored_tables_match_reference's trace and replay, on both caches: victims are chosen by
+    """test_zy_gpu_newest.test_scored_tables_match_reference's trace and replay, on both caches: victims are chosen by
     score and never fall back to LRU, as that test asserts of the device's context."""
     import oracle
     from tierstream_b200 import runtime
@@ -142,7 +142,7 @@ def test_gpu_policies_scored_trace_scores(ref, with_profile):
 
 @pytest.mark.parametrize("wb_defer", [0, 1])
 def test_gpu_policies_rounds_trace_promotes(ref, wb_defer):
-    """test_zzz_gpu_newest.test_rounds_match_reference's trace: its six rounds promote units in the reference replay."""
+    """test_zy_gpu_newest.test_rounds_match_reference's trace: its six rounds promote units in the reference replay."""
     import oracle
     from tierstream_b200 import runtime
     m = model("tsb-test-scored.bin", 13)

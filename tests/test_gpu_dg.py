@@ -2,6 +2,7 @@
 source bytes (the oracle's checksum of the model file), the slot table after every token equals the reference
 DgCore's on the same trace (deterministic schedule), and the failure paths end the token with an error instead of a
 hang."""
+import json
 import os
 
 import numpy as np
@@ -66,10 +67,97 @@ def test_bytes_and_tables_match_reference(small_model, orc, ref, monkeypatch, co
         st = run.ctx.stats()
         assert st["misses"] == s_ref[-1][2] and st["fetched"] == s_ref[-1][4] and st["evicted"] == s_ref[-1][10]
         assert st["misses"] > 20
+        chk = json.loads(run.ctx.stats_json())["check"]  # every landing hashed on the device, none differed
+        assert chk["on"] == 1 and chk["units"] >= st["fetched"] and chk["mismatches"] == 0
         run.ctx.check()
         for L in range(m.layers):
             for u in range(m.units):
                 run.ctx.check_unit(L, u)
+    finally:
+        run.close()
+
+
+def test_c2_part_size_copy_engines_match_reference(orc, ref, monkeypatch):
+    """The benchmark's part size (3 x 33,030,144-byte parts, a 99 MB expert) on the copy-engine
+    mover with stream-written entries and ready words: 4 layers x 8 experts, 3 residents and 1 spare slot per layer,
+    Zipf(1.1) top-2, descriptor hashes checked at the open. After every token the device's slot table equals the
+    reference DgCore's replay, and every routed unit read through the table has the oracle's checksum of its source
+    bytes."""
+    monkeypatch.setenv("TSB_DG_DETERMINISTIC", "1")
+    monkeypatch.setenv("TSB_COPY_MODE", "ce")
+    path = os.path.join(harness.model_dir(), "tsb-test-c2-parts.bin")
+    m = synth.Model(path, layers=4, units=8, part_bytes=(33030144,) * 3, seed=7, top_k=2, with_hash=True)
+    m.write()
+    ids = synth.zipf_trace(24, m.layers, m.units, 2, s=1.1, seed=21)
+    run = harness.DgRun(m, residents_per_layer=3, max_ids=2, verify=True)
+    try:
+        assert '"copy":"copy-engine"' in run.ctx.stats_json()
+        want = {}
+        buf = np.empty(m.unit_bytes, dtype=np.uint8)
+        for k in np.unique((np.arange(m.layers)[None, :, None] * m.units + ids).reshape(-1)):
+            orc.orc_fill_bytes(m.seed, m.unit_offset(int(k) // m.units, int(k) % m.units), m.unit_bytes,
+                               buf.ctypes.data)
+            want[int(k)] = orc.orc_checksum(buf.ctypes.data, m.unit_bytes)
+        t_ref, s_ref = oracle.ref_replay(replay_cfg_for(run, m, ids), ids)
+        for t in range(ids.shape[0]):
+            got = run.step(ids[t])
+            for L in range(m.layers):
+                for i in range(2):
+                    assert int(got[L, i]) == want[L * m.units + int(ids[t, L, i])], "token %d layer %d" % (t, L)
+            assert np.array_equal(run.ctx.table(run.keys), t_ref[t]), "slot table differs after token %d" % t
+        st = run.ctx.stats()
+        assert st["misses"] == s_ref[-1][2] and st["fetched"] == s_ref[-1][4] and st["evicted"] == s_ref[-1][10]
+        assert st["misses"] > 10
+        chk = json.loads(run.ctx.stats_json())["check"]
+        assert chk["on"] == 1 and chk["units"] >= st["fetched"] and chk["mismatches"] == 0
+        run.ctx.check()
+    finally:
+        run.close()
+        for f in (path, path + ".xxh64"):
+            if os.path.exists(f):
+                os.unlink(f)
+
+
+def test_landing_check_reports_and_repairs_a_corrupt_block(small_model, orc):
+    """With verify_hash and descriptor hashes, every unit landed in a slot is hashed on the device and compared with its
+    descriptor hash. A byte flipped in a pinned block (tsb_test_dg_corrupt) lands wrong on the unit's next miss: the
+    ss_end of that token or of one of the next two fails with SS_E_HASH (not poisoned), the unit is read again from
+    its file into its slot and its block, and every later token reads every routed unit's source bytes."""
+    m = small_model
+    run = harness.DgRun(m, residents_per_layer=3, max_ids=2, verify=True)
+    try:
+        want = expected_sums(m, orc)
+        ids = synth.zipf_trace(24, m.layers, m.units, 2, s=1.1, seed=31)
+        for t in range(5):
+            got = run.step(ids[t])
+            keys = np.arange(m.layers)[:, None] * m.units + ids[t]
+            assert np.array_equal(got, want[keys]), "clean token %d read wrong bytes" % t
+        table = run.ctx.table(run.keys)
+        L = 2
+        victim = next(u for u in range(m.units) if table[L * m.units + u] < 0)
+        other = next(u for u in range(m.units) if u != victim)
+        for t in (5, 9):  # routed on the token after the flip, and again after the repair
+            ids[t, L] = [victim, other]
+        abi.check(abi.load().tsb_test_dg_corrupt(run.ctx.h, L, victim, 1000))
+        failed_at = None
+        for t in (5, 6, 7):
+            try:
+                run.step(ids[t])
+            except abi.TsError as e:
+                assert e.status == abi.SS_E_HASH, str(e)
+                assert "(%d, %d)" % (L, victim) in str(e)
+                failed_at = t
+                break
+        assert failed_at is not None, "the flipped byte was not reported by the ss_end of its token or the next two"
+        for t in range(failed_at + 1, ids.shape[0]):
+            got = run.step(ids[t])
+            keys = np.arange(m.layers)[:, None] * m.units + ids[t]
+            assert np.array_equal(got, want[keys]), "token %d after the repair read wrong bytes" % t
+        chk = json.loads(run.ctx.stats_json())["check"]
+        assert chk["on"] == 1 and chk["mismatches"] == 1 and chk["repaired"] >= 1 and chk["units"] > 20
+        run.ctx.check()
+        for u in range(m.units):
+            run.ctx.check_unit(L, u)
     finally:
         run.close()
 

@@ -64,6 +64,7 @@ def test_c1_tables_counters_and_bytes_match_reference(c1_model, orc, ref, dynami
     eng = abi.load_engine()
     want = expected(m, orc)
     s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())  # after the inputs torch made on its own stream
     ids_dev = torch.zeros(m.units, dtype=torch.int32, device="cuda")
     out = torch.zeros(m.units, dtype=torch.int64, device="cuda")
     try:
@@ -129,6 +130,7 @@ def test_layer_all_streams_blobs_through_a_two_slot_ring(orc, ref):
     eng = abi.load_engine()
     want = expected(m, orc)
     s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())  # after the inputs torch made on its own stream
     ids_dev = torch.zeros(1, dtype=torch.int32, device="cuda")
     out = torch.zeros(1, dtype=torch.int64, device="cuda")
     try:
@@ -181,6 +183,7 @@ def test_c1_exclusive_mode_matches_reference(c1_model, orc, ref, dynamic, spare_
     eng = abi.load_engine()
     want = expected(m, orc)
     s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())  # after the inputs torch made on its own stream
     ids_dev = torch.zeros(m.units, dtype=torch.int32, device="cuda")
     out = torch.zeros(m.units, dtype=torch.int64, device="cuda")
     try:
@@ -216,6 +219,7 @@ def run_with_prefetch(m, ctx, routes, pf, mode, ref_locs, ref_stats, want, all_l
     the routes of layer L) and checks tables, the nine counters and the bytes read through the table."""
     eng = abi.load_engine()
     s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())  # after the inputs torch made on its own stream
     ids_dev = torch.zeros(m.units, dtype=torch.int32, device="cuda")
     out = torch.zeros(m.units, dtype=torch.int64, device="cuda")
     keys9 = ("routed", "hits", "admitted", "transient", "evicted", "prefetched", "spec_issued", "spec_used",

@@ -29,6 +29,7 @@ def test_land_host_to_device_any_alignment():
     host = torch.from_numpy(rng.integers(0, 256, size=8 << 20, dtype=np.uint8)).pin_memory()
     dev = torch.zeros(8 << 20, dtype=torch.uint8, device="cuda")
     s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())  # after the inputs torch made on its own stream
     # copies of assorted sizes and offsets, disjoint destinations
     plan, pos = [], 0
     for size in [1, 15, 16, 17, 255, 4096, 65535, 65536, 65537, 1 << 20, 3 * 1000 + 7, 2 << 20]:
@@ -51,6 +52,7 @@ def test_land_publishes_entries_and_ready_after_copies():
     slot_of = torch.full((64,), -1, dtype=torch.int32, device="cuda")
     words = torch.zeros(4, dtype=torch.int32, device="cuda")  # [0] counter, [1] ready
     s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())  # after the inputs torch made on its own stream
     order = rng.permutation(n_units)
     land([host.data_ptr() + int(u) * unit for u in order], [dev.data_ptr() + i * unit for i in range(n_units)],
          [unit] * n_units, s.cuda_stream, slot_of=slot_of.data_ptr(), keys=[int(u) for u in order],
@@ -69,6 +71,7 @@ def test_land_device_to_host_and_device_to_device():
     host = torch.zeros(4 << 20, dtype=torch.uint8).pin_memory()
     dev2 = torch.zeros(4 << 20, dtype=torch.uint8, device="cuda")
     s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())  # after the inputs torch made on its own stream
     half = 2 << 20
     land([src.data_ptr(), src.data_ptr() + half], [host.data_ptr(), dev2.data_ptr() + half], [half, half],
          s.cuda_stream, blocks=7)
@@ -95,6 +98,7 @@ def xxh_units(units, expect=None):
     mism = torch.zeros(1, dtype=torch.int32, device="cuda")
     exp = torch.tensor(np.array(expect, dtype=np.uint64).view(np.int64), device="cuda") if expect else None
     s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())  # the zero fills and the expectations were made on torch's stream
     abi.check(lib.tsb_xxh64_units(spans, sb, ns, n, scratch.data_ptr(), exp.data_ptr() if exp is not None else None,
                                   out.data_ptr(), mism.data_ptr() if exp is not None else None, s.cuda_stream))
     return out.cpu().numpy().view(np.uint64), int(mism.item())
@@ -173,6 +177,7 @@ def test_move_kernel_copies_and_publishes():
     table = torch.full((64,), -1, dtype=torch.int32, device="cuda")
     words = torch.zeros(4, dtype=torch.int32, device="cuda")  # [0] ready, [1] counter
     s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())  # after the inputs torch made on its own stream
     lib = abi.load()
     for rep, (plan, pos) in enumerate(plans):
         assert pos <= src.numel() and pos <= dst.numel()

@@ -218,6 +218,7 @@ def test_allocated_stores_written_on_the_device(model, orc, monkeypatch):
     stores = [peer.Store(desc, owner, r, 0, fill=False) for r in range(2)]
     eng = abi.load_engine()
     s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())  # after the inputs torch made on its own stream
     for r, st in enumerate(stores):
         keys = np.nonzero(owner == r)[0]
         offs = np.array([m.unit_offset(int(k) // m.units, int(k) % m.units) for k in keys], dtype=np.uint64)

@@ -178,6 +178,7 @@ def test_host_read_ahead_lands_file_blobs(orc, ra):
     eng = abi.load_engine()
     want = expected(m, orc)
     s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())  # after the inputs torch made on its own stream
     ids_dev = torch.zeros(1, dtype=torch.int32, device="cuda")
     out = torch.zeros(1, dtype=torch.int64, device="cuda")
     try:

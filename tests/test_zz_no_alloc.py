@@ -69,6 +69,8 @@ def test_static_table_matches_caller_scratch_twice(orc):
         mism_a = torch.zeros(1, dtype=torch.int32, device="cuda")
         mism_b = torch.zeros(1, dtype=torch.int32, device="cuda")
         scratch = torch.zeros(n * 72 // 8 + 1, dtype=torch.int64, device="cuda")
+        # the zero fills and the planted mismatch ran on torch's current stream: the calls' stream waits for them
+        s.wait_stream(torch.cuda.current_stream())
         abi.check(lib.tsb_xxh64_units(spans, sb, ns, n, scratch.data_ptr(), exp.data_ptr(), out_a.data_ptr(),
                                       mism_a.data_ptr(), s.cuda_stream))
         abi.check(lib.tsb_xxh64_units_static(spans, sb, ns, n, exp.data_ptr(), out_b.data_ptr(), mism_b.data_ptr(),

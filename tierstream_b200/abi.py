@@ -272,6 +272,7 @@ _PROTOS = {
     "tsb_dg_peer_retier": (C.c_int, [vp, P(tsb_peer_tier)]),
     "tsb_test_dg_replay": (C.c_int, [P(dg_replay_config), P(i32), P(i32), P(i32), P(u64), P(C.c_uint8), P(u64)]),
     "tsb_test_dg_table": (C.c_int, [vp, P(i32), u32]),
+    "tsb_test_dg_corrupt": (C.c_int, [vp, C.c_int, C.c_int, u64]),
     "tsb_xxh64": (u64, [vp, C.c_size_t, u64]),
     "tsb_test_host_locs": (C.c_int, [vp, C.c_int, P(i32), C.c_int]),
     "ss_layer_routes_dev": (C.c_int, [vp, C.c_int, vp, C.c_int, vp]),
@@ -286,6 +287,7 @@ _ENGINE_PROTOS = {
     "tse_fill_bytes": (None, [u64, u64, u64, vp, u32]),
     "tse_fill_units_device": (C.c_int, [u64, P(u64), u32, u64, vp, vp]),
     "tse_read_table": (C.c_int, [vp, vp, u32, u64, vp, u32, vp]),
+    "tse_expect_sums": (C.c_int, [u64, vp, u32, u64, C.c_int, vp, u32, vp]),
 }
 
 _lib = None

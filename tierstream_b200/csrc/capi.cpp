@@ -631,6 +631,11 @@ ss_status tsb_test_dg_table(ss_ctx* c, int32_t* out, uint32_t cap) {
   return guard([&] { dg_of(c, "tsb_test_dg_table").test_table(out, cap); });
 }
 
+ss_status tsb_test_dg_corrupt(ss_ctx* c, int layer, int unit, uint64_t offset) {
+  if (!c) return SS_E_INVALID;
+  return guard([&] { dg_of(c, "tsb_test_dg_corrupt").test_corrupt(layer, unit, offset); });
+}
+
 ss_status tsb_test_host_locs(ss_ctx* c, int layer, int32_t* out, int n) {
   if (!c || !out) return SS_E_INVALID;
   return guard([&] { host_of(c, "tsb_test_host_locs").test_locs(layer, out, n); });

@@ -86,6 +86,8 @@ class DgContext {
   virtual uint32_t test_coming() = 0;
   virtual void test_stop_service() = 0;
   virtual uint32_t test_table(int32_t* out, uint32_t cap) = 0;  // the device's slot table; returns the key count
+  // flips the byte at `offset` of the unit's pinned block (a Host home with a block), between tokens
+  virtual void test_corrupt(int layer, int unit, uint64_t offset) = 0;
 };
 
 struct PeerTier;

@@ -339,6 +339,12 @@ class CudaMover final : public Mover {
   ~CudaMover() override {
     for (cudaStream_t s : s_)
       if (s) cudaStreamSynchronize(s);
+    for (cudaStream_t s : chk_.vs)
+      if (s) cudaStreamSynchronize(s);
+    for (cudaEvent_t e : chk_.land_ev)
+      if (e) cudaEventDestroy(e);
+    for (cudaStream_t s : chk_.vs)
+      if (s) cudaStreamDestroy(s);
     if (table_pin_) cudaFreeHost(table_pin_);
     for (cudaEvent_t e : ev_a_)
       if (e) cudaEventDestroy(e);
@@ -360,6 +366,7 @@ class CudaMover final : public Mover {
   uint64_t part_bytes(uint32_t p) const override { return x_.part_bytes[p]; }
 
   void h2d(Stream s, int32_t slot, int32_t block, uint32_t key) override {
+    check_hold(s, slot);
     if (peer_ && peer_->owned(key)) {  // from the owner's store: NVLink for a peer, HBM for this GPU's own
       const char* src = peer_->src(key, x_.unit_bytes);
       const bool self = peer_->owner[key] == peer_->rank;
@@ -373,10 +380,11 @@ class CudaMover final : public Mover {
         }
       }
       ++(self ? self_units_ : peer_units_);
-      return;
+    } else {
+      for (uint32_t p = 0; p < parts(); ++p)
+        copy(s, block_dev(block) + x_.part_offset[p], arena(p, slot), x_.part_bytes[p], cudaMemcpyHostToDevice);
     }
-    for (uint32_t p = 0; p < parts(); ++p)
-      copy(s, block_dev(block) + x_.part_offset[p], arena(p, slot), x_.part_bytes[p], cudaMemcpyHostToDevice);
+    check_add(s, key, slot);
   }
   void d2h(Stream s, int32_t slot, int32_t block, int32_t part, uint32_t key) override {
     if (peer_ && peer_->owned(key)) return;  // its store keeps its bytes: the block is bookkeeping only
@@ -387,6 +395,7 @@ class CudaMover final : public Mover {
   }
   void d2d_moves(const std::vector<std::pair<int32_t, int32_t>>& moves, const std::vector<uint32_t>& wave) override {
     flush(kDem);
+    check_fence(kDem);  // no move overwrites a slot whose landing is still being hashed
     uint32_t max_wave = 0;
     for (uint32_t w : wave) max_wave = std::max(max_wave, w);
     // K4 (TMA bulk copies through shared memory) per wave, stream-ordered on kDem; the arena's parts are 256-byte
@@ -464,12 +473,13 @@ class CudaMover final : public Mover {
       b.ready_word = b_.ready + g;
       b.ready_val = seq;
       flush(kDem, true);
-      return;
+    } else {
+      flush(kDem);
+      ck_drv(write_value32(reinterpret_cast<CUstream>(s_[kDem]), reinterpret_cast<CUdeviceptr>(b_.ready + g),
+                           cuuint32_t(seq)),
+             "cuStreamWriteValue32 (ready)");
     }
-    flush(kDem);
-    ck_drv(write_value32(reinterpret_cast<CUstream>(s_[kDem]), reinterpret_cast<CUdeviceptr>(b_.ready + g),
-                         cuuint32_t(seq)),
-           "cuStreamWriteValue32 (ready)");
+    check_submit(kDem);  // behind the ready word: the engine never waits for the check
   }
   void* event_create() override {
     cudaEvent_t e = nullptr;
@@ -482,6 +492,7 @@ class CudaMover final : public Mover {
   void record(void* ev, Stream s) override {
     flush(s);
     ck(cudaEventRecord(static_cast<cudaEvent_t>(ev), s_[s]), "cudaEventRecord");
+    check_submit(s);
   }
   void wait(Stream s, void* ev) override {
     flush(s);
@@ -500,6 +511,7 @@ class CudaMover final : public Mover {
   void event_sync(void* ev) override { ck(cudaEventSynchronize(static_cast<cudaEvent_t>(ev)), "cudaEventSynchronize"); }
   void sync(Stream s) override {
     flush(s);
+    check_submit(s);
     ck(cudaStreamSynchronize(s_[s]), "cudaStreamSynchronize");
   }
   void upload_table(const int32_t* t, uint32_t n) override {
@@ -549,7 +561,201 @@ class CudaMover final : public Mover {
   double dma_ms(uint32_t g) const { return g < dma_ms_.size() ? dma_ms_[g] : -1; }
   double dma_total_ms() const { return dma_total_ms_; }
 
+  // ---- The landing check (verify_hash with descriptor hashes) ----
+  // Every unit copied into a slot (demand, prefetch, placement round, kept-resident set; from a pinned block, a staging
+  // buffer or a peer store) is hashed on the device by K3 over the landed slot, after the copies of its stream (after
+  // the layer's ready word for demand copies, so the engine never waits for it), and compared with its descriptor hash;
+  // a mismatch is logged in mapped memory for the host. One unit's hash is a serial chain (about 70 ms for a 99 MB
+  // unit), so launches run side by side on a pool of low-priority streams, a launch on a stream whose last launch has
+  // finished. When every stream is busy, landings stay pending and join the next launch (a launch hashes all its units
+  // at once), so the hashing keeps up with any landing rate without the host waiting: the boundary submits what is left.
+  // Launches are numbered; each one's last CTA writes its number to its word of a mapped ring when it finished (no event
+  // is recorded after a hash: an event record behind a 70 ms kernel would hold every stream that shares its hardware
+  // queue). slot_gen[slot] is the last launch that reads a slot; a copy into a slot whose landing is pending or being
+  // hashed first submits it and waits for it on the host, so a hash never reads a slot being overwritten. Nothing here
+  // changes a decision of the slot cache.
+  struct CheckWords {
+    const uint64_t* expect;  // [keys], device
+    uint32_t* bad_count;     // device
+    uint32_t* bad_log;       // mapped, device address
+    uint32_t* bad_flag;      // mapped, device address
+    uint32_t* timeouts;      // device
+    uint32_t* done_cnt;      // device, kCheckRing words (zeroed)
+    uint32_t* done_dev;      // mapped, kCheckRing words: device address
+    const uint32_t* done_host;  // the same words: host address
+  };
+  static constexpr uint32_t kCheckRing = 256;
+  struct CheckStats {
+    uint64_t units = 0, bytes = 0, launches = 0, hold_waits = 0, merged = 0;
+  };
+  void enable_check(const CheckWords& w) {
+    int lo = 0, hi = 0;
+    ck(cudaDeviceGetStreamPriorityRange(&lo, &hi), "cudaDeviceGetStreamPriorityRange");
+    chk_.vs.assign(kCheckStreams, nullptr);
+    chk_.last_on.assign(kCheckStreams, 0);
+    for (cudaStream_t& v : chk_.vs)
+      ck(cudaStreamCreateWithPriority(&v, cudaStreamNonBlocking, lo), "cudaStreamCreate (landing check)");
+    chk_.land_ev.assign(kCheckRing, nullptr);
+    for (uint32_t i = 0; i < kCheckRing; ++i)
+      ck(cudaEventCreateWithFlags(&chk_.land_ev[i], cudaEventDisableTiming), "cudaEventCreate (landing check)");
+    chk_.slot_gen.assign(x_.slots, 0);
+    chk_.slot_pending.assign(x_.slots, 0);
+    chk_.w = w;
+    chk_.on = true;
+  }
+  bool check_on() const { return chk_.on; }
+  const CheckStats& check_stats() const { return chk_.st; }
+  // Every landing so far submitted (on busy streams too), and the number of the last launch (a mark for check_wait).
+  uint64_t check_mark() {
+    for (Stream st : {kDem, kPf, kD2h}) check_submit(st, true);
+    return chk_.launched;
+  }
+  // Host wait until every launch up to `mark` finished; returns the seconds waited.
+  double check_wait(uint64_t mark) {
+    if (!chk_.on || mark <= chk_.completed) return 0;
+    check_poll();
+    if (mark <= chk_.completed) return 0;
+    const auto t0 = Clock::now();
+    check_complete_through(mark);
+    return std::chrono::duration<double>(Clock::now() - t0).count();
+  }
+  // Every landing submitted and hashed.
+  void check_drain() {
+    if (!chk_.on) return;
+    check_wait(check_mark());
+    for (cudaStream_t v : chk_.vs) ck(cudaStreamSynchronize(v), "cudaStreamSynchronize (landing check)");
+  }
+
  private:
+  static constexpr uint32_t kCheckStreams = 32;
+  // Launch i finished: its done word holds i (or a later launch of the same ring entry).
+  bool check_done(uint64_t i) const {
+    return int32_t(load_acquire(chk_.w.done_host + i % kCheckRing) - uint32_t(i)) >= 0;
+  }
+  // Host wait until launch i finished (its hash waits are bounded, so it does: a launch silent for 30 s is a device
+  // failure).
+  void check_wait_one(uint64_t i) {
+    if (check_done(i)) return;
+    const auto deadline = Clock::now() + std::chrono::seconds(30);
+    for (uint32_t spins = 0; !check_done(i); ++spins) {
+      if ((spins & 1023u) == 0) {
+        require(Clock::now() < deadline, SS_E_BACKEND, "device-gated: a landing check launch did not finish in 30 s");
+        ck(cudaGetLastError(), "landing check");
+      }
+      if (spins < 4096) cpu_relax();
+      else std::this_thread::yield();
+    }
+  }
+  // Host wait for launches completed + 1 .. last.
+  void check_complete_through(uint64_t last) {
+    for (uint64_t i = chk_.completed + 1; i <= last; ++i) check_wait_one(i);
+    chk_.completed = std::max(chk_.completed, last);
+  }
+  void check_poll() {
+    while (chk_.completed < chk_.launched && check_done(chk_.completed + 1)) ++chk_.completed;
+  }
+  // Before a copy into `slot` on s: the slot's last landing has been hashed (its pending landing is submitted first; a
+  // host wait, rare: a slot is reused long after its unit landed unless it is a bank slot).
+  void check_hold(Stream s, int32_t slot) {
+    if (!chk_.on) return;
+    if (const uint8_t ps = chk_.slot_pending[size_t(slot)]) check_submit(Stream(ps - 1), true);
+    const uint64_t g = chk_.slot_gen[size_t(slot)];
+    if (g <= chk_.completed) return;
+    check_poll();
+    if (g <= chk_.completed || check_done(g)) return;
+    ++chk_.st.hold_waits;
+    flush(s);  // copies already batched on s do not wait
+    check_wait_one(g);
+  }
+  // Before copies that may overwrite any slot (reset moves): every landing hashed.
+  void check_fence(Stream s) {
+    (void)s;
+    if (!chk_.on) return;
+    check_complete_through(check_mark());
+  }
+  void check_add(Stream s, uint32_t key, int32_t slot) {
+    if (!chk_.on) return;
+    chk_.pending[s].push_back({key, slot});
+    chk_.slot_pending[size_t(slot)] = uint8_t(s + 1);
+    if (chk_.pending[s].size() == dev::kMaxVerify) check_submit(s, true);
+  }
+  // One K3 launch over the landings pending on s, behind everything enqueued on s so far, on a check stream whose last
+  // launch finished; with none free the landings stay pending unless `force` (then the stream whose last launch is the
+  // oldest takes it, queued behind that launch).
+  void check_submit(Stream s, bool force = false) {
+    auto& p = chk_.pending[s];
+    if (!chk_.on || p.empty()) return;
+    uint32_t pick = kCheckStreams;
+    for (uint32_t k = 0; k < kCheckStreams && pick == kCheckStreams; ++k) {
+      const uint32_t i = (chk_.rr + k) % kCheckStreams;
+      if (!chk_.last_on[i] || check_done(chk_.last_on[i])) pick = i;
+    }
+    if (pick == kCheckStreams) {
+      if (!force) {
+        ++chk_.st.merged;
+        return;
+      }
+      pick = 0;
+      for (uint32_t i = 1; i < kCheckStreams; ++i)
+        if (chk_.last_on[i] < chk_.last_on[pick]) pick = i;
+    }
+    chk_.rr = (pick + 1) % kCheckStreams;
+    flush(s);
+    const uint64_t n = chk_.launched + 1;
+    if (n > kCheckRing && chk_.completed < n - kCheckRing) {  // the ring's words of launch n - R are reused for n
+      check_poll();
+      if (chk_.completed < n - kCheckRing) check_complete_through(n - kCheckRing);
+    }
+    cudaStream_t vs = chk_.vs[pick];
+    cudaEvent_t le = chk_.land_ev[n % kCheckRing];
+    ck(cudaEventRecord(le, s_[s]), "cudaEventRecord (landing check)");
+    ck(cudaStreamWaitEvent(vs, le, 0), "cudaStreamWaitEvent (landing check)");
+    dev::VerifyBatch& b = *chk_.batch;
+    b.n_parts = parts();
+    for (uint32_t q = 0; q < b.n_parts; ++q) {
+      b.arena[q] = reinterpret_cast<const uint8_t*>(b_.arena[q]);
+      b.part_bytes[q] = x_.part_bytes[q];
+    }
+    b.n = uint32_t(p.size());
+    b.expect = chk_.w.expect;
+    b.bad_count = chk_.w.bad_count;
+    b.bad_log = chk_.w.bad_log;
+    b.bad_flag = chk_.w.bad_flag;
+    b.timeouts = chk_.w.timeouts;
+    b.done_cnt = chk_.w.done_cnt + n % kCheckRing;
+    b.done_word = chk_.w.done_dev + n % kCheckRing;
+    b.done_val = uint32_t(n);
+    for (uint32_t i = 0; i < b.n; ++i) {
+      b.key[i] = p[i].first;
+      b.slot[i] = p[i].second;
+    }
+    ck_launch(dev::launch_xxh64_landed(b, vs), "xxh64 kernel (landing check)");
+    chk_.launched = n;
+    chk_.last_on[pick] = n;
+    for (const auto& [key, slot] : p) {
+      chk_.slot_gen[size_t(slot)] = n;
+      chk_.slot_pending[size_t(slot)] = 0;
+    }
+    chk_.st.units += p.size();
+    chk_.st.bytes += p.size() * x_.unit_bytes;
+    ++chk_.st.launches;
+    p.clear();
+  }
+  struct Check {
+    bool on = false;
+    std::vector<cudaStream_t> vs;
+    std::vector<uint64_t> last_on;  // per check stream: its last launch (0: none)
+    uint32_t rr = 0;                // where the search for a free stream starts
+    CheckWords w{};
+    std::vector<cudaEvent_t> land_ev;
+    std::vector<uint64_t> slot_gen;
+    std::vector<uint8_t> slot_pending;  // per slot: 1 + the copy stream of its pending landing, 0 = none
+    std::vector<std::pair<uint32_t, int32_t>> pending[3];
+    uint64_t launched = 0, completed = 0;
+    std::unique_ptr<dev::VerifyBatch> batch = std::make_unique<dev::VerifyBatch>();
+    CheckStats st;
+  } chk_;
+
   char* arena(uint32_t p, int32_t slot) const { return b_.arena[p] + uint64_t(slot) * x_.part_bytes[p]; }
   char* block_dev(int32_t b) const { return b < 0 ? b_.staging_d : b_.blocks_d[size_t(b)]; }
   char* block_host(int32_t b) const { return b < 0 ? b_.staging : b_.blocks[size_t(b)]; }
@@ -930,6 +1136,71 @@ class CudaDgContext final : public DgContext {
     boundary_.select_us = us_between(t0, Clock::now());
     if (o_.dg_diag) collect_diag();
     timeline_valid_ = true;
+    if (mover_->check_on()) end_check();
+  }
+
+  // The landing check at ss_end: this token's landings are submitted, and those of the token before the previous one
+  // have been hashed before the call returns, so a unit that landed wrong fails the ss_end of its own token or of one
+  // of the next two (a 99 MB unit's hash takes longer than a token: waiting for the previous token's would stall). A
+  // mismatch fails it with SS_E_HASH (a library error: the context stays usable) once every unit logged has been read
+  // again from its file into its slot and, when it has one, its pinned block; the outputs of both tokens must be
+  // discarded. A staging copy of the check that did not complete, or more mismatches than the log holds, is a device
+  // failure (SS_E_BACKEND).
+  void end_check() {
+    const uint64_t mark = mover_->check_mark();
+    check_wait_s_ += mover_->check_wait(check_marks_[0]);
+    check_marks_[0] = check_marks_[1];
+    check_marks_[1] = mark;
+    if (!load_acquire(bad_flag_h_)) return;
+    mover_->check_drain();  // every check issued so far has finished: the log is complete and nothing writes it
+    uint32_t count = 0, touts = 0;
+    ck(cudaMemcpy(&count, ctl_ + 6, 4, cudaMemcpyDeviceToHost), "cudaMemcpy (landing check)");
+    ck(cudaMemcpy(&touts, ctl_ + 7, 4, cudaMemcpyDeviceToHost), "cudaMemcpy (landing check)");
+    std::vector<std::pair<uint32_t, int32_t>> bad;
+    for (uint32_t i = 0; i < std::min(count, dev::kBadLog); ++i)
+      bad.push_back({bad_log_h_[2 * i], int32_t(bad_log_h_[2 * i + 1])});
+    ck(cudaMemset(ctl_ + 6, 0, 8), "cudaMemset (landing check)");
+    store_release(bad_flag_h_, 0);
+    check_failed_ += count;
+    if (touts || count > dev::kBadLog) {
+      poisoned_ = true;
+      fail(SS_E_BACKEND, touts ? "device-gated: a staging copy of the landing check did not complete in 2 s"
+                               : "device-gated: " + std::to_string(count) +
+                                     " landed units differ from their descriptor hashes, more than the check logs");
+    }
+    std::sort(bad.begin(), bad.end());
+    bad.erase(std::unique(bad.begin(), bad.end(), [](auto& a, auto& b) { return a.first == b.first; }), bad.end());
+    std::string names;
+    for (const auto& [key, slot] : bad) {
+      const uint32_t g = core_->gated_of(key);
+      const int layer = x_.gated[g], unit = int(key - x_.unit_base[g]);
+      names += (names.empty() ? "(" : ", (") + std::to_string(layer) + ", " + std::to_string(unit) + ")";
+      repair(key);
+    }
+    fail(SS_E_HASH, "device-gated: landed bytes of unit(s) " + names +
+                        " differ from their descriptor hashes (read again from their files; the outputs of this token and "
+                        "the two before it must be discarded)");
+  }
+
+  // A unit whose landed bytes were wrong: every copy this context keeps of it (its slot, its pinned block) read again
+  // from its file, checked against its descriptor hash on the host. Between tokens; the service is idle and every
+  // landing check has finished.
+  void repair(uint32_t key) {
+    const uint32_t g = core_->gated_of(key);
+    const int layer = x_.gated[g], unit = int(key - x_.unit_base[g]);
+    const bool owned = peer_ && peer_->owned(key);
+    const int32_t slot = core_->slot_of(key), block = core_->block_of(key);
+    const bool in_slot = slot >= 0 && core_->home(key) != SlotCache::Home::Host && core_->home(key) != SlotCache::Home::File;
+    if (!in_slot && (block < 0 || owned)) return;
+    std::vector<char> bytes(size_t(x_.unit_bytes));
+    read_checked(layer, unit, bytes.data(), readers_ != nullptr);
+    if (in_slot)
+      for (size_t p = 0; p < x_.part_bytes.size(); ++p)
+        ck(cudaMemcpy(unit_part_dst(slot, uint32_t(p)), bytes.data() + x_.part_offset[p], size_t(x_.part_bytes[p]),
+                      cudaMemcpyHostToDevice),
+           "cudaMemcpy (repair)");
+    if (block >= 0 && !owned) std::memcpy(bufs_.blocks[size_t(block)], bytes.data(), bytes.size());
+    ++check_repaired_;
   }
 
   void seed(int layer, const int32_t* units, int n) override {
@@ -1260,7 +1531,7 @@ class CudaDgContext final : public DgContext {
   std::string stats_json() const override {
     ss_dg_stats s;
     stats(&s);
-    char buf[3072];
+    char buf[4096];
     std::snprintf(buf, sizeof buf,
                   "{\"schema\":\"strix-stream/stats-v1\",\"mode\":\"device-gated\",\"copy\":\"%s\","
                   "\"dg\":{\"tokens\":%llu,\"lookups\":%llu,\"misses\":%llu,\"covered\":%llu,\"fetched\":%llu,"
@@ -1274,7 +1545,9 @@ class CudaDgContext final : public DgContext {
                   "\"fill_s\":%.3f,\"fill_pinned_s\":%.3f,\"fill_residents_s\":%.3f,\"verify_s\":%.3f,"
                   "\"load\":\"%s\",\"load_readers\":%u,\"load_buffers\":%u,\"load_buffer_bytes\":%llu,"
                   "\"load_batches\":%llu,\"load_slot_units\":%llu,\"load_pinned_units\":%llu,"
-                  "\"load_reader_waits\":%llu,\"load_recycles\":%llu,\"load_residents_submitted_s\":%.3f}}",
+                  "\"load_reader_waits\":%llu,\"load_recycles\":%llu,\"load_residents_submitted_s\":%.3f},"
+                  "\"check\":{\"on\":%d,\"units\":%llu,\"bytes\":%llu,\"launches\":%llu,\"merged\":%llu,\"hold_waits\":%llu,"
+                  "\"mismatches\":%llu,\"repaired\":%llu,\"end_wait_s\":%.6f}}",
                   mover_->kernel_copies() ? "land-kernel" : "copy-engine", (unsigned long long)s.tokens,
                   (unsigned long long)s.lookups, (unsigned long long)s.misses, (unsigned long long)s.covered,
                   (unsigned long long)s.fetched, (unsigned long long)s.prefetched, (unsigned long long)s.bank_serves,
@@ -1291,7 +1564,12 @@ class CudaDgContext final : public DgContext {
                   open_verify_s_, load_serial_ ? "serial" : "pipeline", load_readers_, load_buffers_,
                   (unsigned long long)load_buffer_bytes_, (unsigned long long)load_.batches,
                   (unsigned long long)load_.slot_units, (unsigned long long)load_.host_units,
-                  (unsigned long long)load_.reader_waits, (unsigned long long)load_.recycles, load_.slot_seconds);
+                  (unsigned long long)load_.reader_waits, (unsigned long long)load_.recycles, load_.slot_seconds,
+                  mover_->check_on() ? 1 : 0, (unsigned long long)mover_->check_stats().units,
+                  (unsigned long long)mover_->check_stats().bytes, (unsigned long long)mover_->check_stats().launches,
+                  (unsigned long long)mover_->check_stats().merged,
+                  (unsigned long long)mover_->check_stats().hold_waits, (unsigned long long)check_failed_,
+                  (unsigned long long)check_repaired_, check_wait_s_);
     return buf;
   }
   void reset_open() override {
@@ -1378,6 +1656,18 @@ class CudaDgContext final : public DgContext {
   void test_stop_service() override {
     hooks("ss_test_dg_stop_service");
     svc_->stop_join();
+  }
+  void test_corrupt(int layer, int unit, uint64_t offset) override {
+    hooks("tsb_test_dg_corrupt");
+    require(!in_token_, SS_E_INVALID, "tsb_test_dg_corrupt: between tokens only");
+    const int g = gated_index(layer);
+    require(g >= 0 && unit >= 0 && uint32_t(unit) < core_->units(uint32_t(g)), SS_E_INVALID,
+            "tsb_test_dg_corrupt: not a gated unit");
+    const uint32_t k = core_->key(uint32_t(g), uint32_t(unit));
+    require(core_->home(k) == SlotCache::Home::Host && core_->block_of(k) >= 0 && !(peer_ && peer_->owned(k)),
+            SS_E_INVALID, "tsb_test_dg_corrupt: the unit is not in a pinned block");
+    require(offset < x_.unit_bytes, SS_E_INVALID, "tsb_test_dg_corrupt: offset beyond the unit");
+    bufs_.blocks[size_t(core_->block_of(k))][offset] ^= char(0x5a);
   }
   uint32_t test_table(int32_t* out, uint32_t cap) override {
     hooks("tsb_test_dg_table");
@@ -1503,7 +1793,9 @@ class CudaDgContext final : public DgContext {
     // the mapped control area, 64-byte aligned pieces
     const size_t rec_b = size_t(G) * sizeof(dev::DgRecord), prec_b = size_t(G) * sizeof(dev::DgPredRecord);
     auto r64 = [](size_t n) { return (n + 63) / 64 * 64; };
-    const size_t mapped_bytes = r64(rec_b) + r64(prec_b) + 2 * r64(size_t(G) * 4) + 64;
+    // the landing check's flag, log and launch done words
+    const size_t check_b = (1 + 2 * size_t(dev::kBadLog) + CudaMover::kCheckRing) * 4;
+    const size_t mapped_bytes = r64(rec_b) + r64(prec_b) + 2 * r64(size_t(G) * 4) + 64 + r64(check_b);
     ck(cudaHostAlloc(&mapped_h_, mapped_bytes, cudaHostAllocMapped | cudaHostAllocPortable), "cudaHostAlloc (mapped)");
     std::memset(mapped_h_, 0, mapped_bytes);
     void* md = nullptr;
@@ -1535,6 +1827,10 @@ class CudaDgContext final : public DgContext {
     dev_.host_seq = words_d + 4;
     dev_.began = words_d + 5;
     dev_.m_err_count = words_d + 6;
+    uint32_t *chk_h = nullptr, *chk_d = nullptr;
+    carve(check_b, &chk_h, &chk_d);
+    bad_flag_h_ = chk_h;
+    bad_log_h_ = chk_h + 1;
     if (o_.dg_diag) {
       void* h = nullptr;
       ck(cudaHostAlloc(&h, size_t(G) * 32, cudaHostAllocMapped | cudaHostAllocPortable), "cudaHostAlloc (stamps)");
@@ -1579,6 +1875,31 @@ class CudaDgContext final : public DgContext {
     // the cache: residents in slots 0.., every other unit in a block
     mover_ = std::make_unique<CudaMover>(x_, bufs_, peer_.get());
     if (o_.dg_diag) mover_->enable_diag(G);
+    // the landing check: with verify_hash and a hash for every gated unit, every unit landed in a slot is hashed on the
+    // device and compared with its descriptor hash (ss_end reports a mismatch)
+    bool hashed = o_.verify_hash != 0;
+    for (int L : x_.gated) hashed = hashed && !d_.layers[size_t(L)].hash.empty();
+    if (hashed) {
+      std::vector<uint64_t> expect;
+      expect.reserve(x_.keys);
+      for (int L : x_.gated)
+        expect.insert(expect.end(), d_.layers[size_t(L)].hash.begin(), d_.layers[size_t(L)].hash.end());
+      ck(cudaMalloc(reinterpret_cast<void**>(&expect_dev_), expect.size() * 8), "cudaMalloc (descriptor hashes)");
+      ck(cudaMemcpy(expect_dev_, expect.data(), expect.size() * 8, cudaMemcpyHostToDevice),
+         "cudaMemcpy (descriptor hashes)");
+      ck(cudaMalloc(reinterpret_cast<void**>(&done_cnt_), CudaMover::kCheckRing * 4), "cudaMalloc (landing check)");
+      ck(cudaMemset(done_cnt_, 0, CudaMover::kCheckRing * 4), "cudaMemset (landing check)");
+      CudaMover::CheckWords w{};
+      w.expect = expect_dev_;
+      w.bad_count = ctl_ + 6;
+      w.timeouts = ctl_ + 7;
+      w.bad_flag = chk_d;
+      w.bad_log = chk_d + 1;
+      w.done_cnt = done_cnt_;
+      w.done_dev = chk_d + 1 + 2 * dev::kBadLog;
+      w.done_host = bad_flag_h_ + 1 + 2 * dev::kBadLog;
+      mover_->enable_check(w);
+    }
     CacheConfig c;
     for (int L : x_.gated) c.n_units.push_back(uint32_t(d_.layers[size_t(L)].n_units));
     c.persistent_slots = x_.persistent_slots;
@@ -1908,6 +2229,8 @@ class CudaDgContext final : public DgContext {
     readers_.reset();
     for (char* a : bufs_.arena) cudaFree(a);
     if (bufs_.slot_of) cudaFree(bufs_.slot_of);
+    if (expect_dev_) cudaFree(expect_dev_);
+    if (done_cnt_) cudaFree(done_cnt_);
     if (ctl_) cudaFree(ctl_);
     if (mapped_h_) cudaFreeHost(mapped_h_);
     if (stamps_h_) cudaFreeHost(stamps_h_);
@@ -1927,6 +2250,13 @@ class CudaDgContext final : public DgContext {
   std::unique_ptr<AsyncReads> async_;                        // file tier: reads in flight (dg_disk_queue > 1)
   CudaMover::Buffers bufs_;
   uint32_t* ctl_ = nullptr;
+  uint64_t* expect_dev_ = nullptr;  // the landing check: descriptor hashes in key order
+  uint32_t* done_cnt_ = nullptr;    // the landing check: CTAs finished per launch ring entry
+  uint32_t* bad_flag_h_ = nullptr;  // mapped: set by a mismatch
+  uint32_t* bad_log_h_ = nullptr;   // mapped: (key, slot) of the first mismatches
+  uint64_t check_marks_[2] = {0, 0};  // the last check launch of the two previous tokens
+  uint64_t check_failed_ = 0, check_repaired_ = 0;
+  double check_wait_s_ = 0;
   void* mapped_h_ = nullptr;
   unsigned long long* stamps_h_ = nullptr;
   std::vector<void*> chunks_;       // the block chunks' host addresses

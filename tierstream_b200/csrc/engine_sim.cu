@@ -25,6 +25,22 @@ __device__ __forceinline__ uint64_t warp_sum(uint64_t v) {
   return v;
 }
 
+// sum over k < 16 of byte k x ((m + k) % 251 + 1) for the 16 bytes of w (m < 251): (m + 1) x sum(b) + sum(k x b) from
+// byte dot products, less 251 x b for the bytes past the wrap (k >= 251 - m, only when m > 235).
+__device__ __forceinline__ uint64_t weighted16(const uint4& w, uint32_t m) {
+  const uint32_t words[4] = {w.x, w.y, w.z, w.w};
+  uint32_t s0 = 0, s1 = 0;
+#pragma unroll
+  for (uint32_t j = 0; j < 4; ++j) {
+    s0 = __dp4a(words[j], 0x01010101u, s0);
+    s1 = __dp4a(words[j], 0x03020100u + 0x04040404u * j, s1);
+  }
+  uint64_t v = uint64_t(m + 1) * s0 + s1;
+  if (m > 235)
+    for (uint32_t k = 251 - m; k < 16; ++k) v -= 251ull * ((words[k >> 2] >> (8 * (k & 3))) & 0xffu);
+  return v;
+}
+
 // grid (n, slices): block (i, s) reads slice s of unit ids[i] of gated layer g and adds its part of the checksum.
 __global__ __launch_bounds__(kThreads) void reader_kernel(ss_dg_device_view v, uint32_t g, const int32_t* ids,
                                                           uint32_t n, unsigned long long* out, int mode) {
@@ -38,8 +54,12 @@ __global__ __launch_bounds__(kThreads) void reader_kernel(ss_dg_device_view v, u
   const uint64_t per = (n16 + gridDim.y - 1) / gridDim.y;
   const uint64_t lo = per * blockIdx.y, hi = lo + per < n16 ? lo + per : n16;
   uint64_t acc = 0;
+  // mode 0: the group at position pos weighs its byte k by (pos + k) % 251 + 1; m = pos % 251 steps by
+  // 16 x kThreads % 251 per iteration
+  constexpr uint32_t kStep = (16u * kThreads) % 251u;
+  uint32_t m = uint32_t(((lo + threadIdx.x) * 16) % 251);
   for (uint64_t e = lo + threadIdx.x; e < hi; e += kThreads) {
-    uint64_t pos = e * 16;  // position in the unit's bytes
+    const uint64_t pos = e * 16;  // position in the unit's bytes
     uint32_t p = 0;
     uint64_t off = pos;
     while (p + 1 < v.n_parts && off >= v.parts[p].bytes) {
@@ -52,13 +72,9 @@ __global__ __launch_bounds__(kThreads) void reader_kernel(ss_dg_device_view v, u
       acc += uint64_t(w.x) + w.y + w.z + w.w;
       continue;
     }
-    const uint32_t words[4] = {w.x, w.y, w.z, w.w};
-    uint32_t m = uint32_t(pos % 251);
-#pragma unroll
-    for (int k = 0; k < 16; ++k) {
-      acc += uint64_t((words[k >> 2] >> (8 * (k & 3))) & 0xffu) * (m + 1);
-      m = m + 1 == 251 ? 0 : m + 1;
-    }
+    acc += weighted16(w, m);
+    m += kStep;
+    if (m >= 251) m -= 251;
   }
   __shared__ uint64_t part[kThreads / 32];
   acc = warp_sum(acc);
@@ -200,6 +216,15 @@ __attribute__((visibility("default"))) void tse_fill_bytes(uint64_t file_id, uin
   for (auto& t : th) t.join();
 }
 
+// Byte i of file `file_id` of the synthetic stream (the same formula as tse_fill_bytes), on the device.
+__device__ __forceinline__ uint8_t gen_byte(uint64_t file_id, uint64_t i) {
+  uint64_t x = (i + 1) * 0x9E3779B97F4A7C15ULL ^ (file_id + 7) * 0xC2B2AE3D27D4EB4FULL;
+  x ^= x >> 29;
+  x *= 0xBF58476D1CE4E5B9ULL;
+  x ^= x >> 32;
+  return uint8_t(x);
+}
+
 // The same byte stream written on the device: n bytes of file `file_id` from position `first` into dst (HBM), for a
 // store the caller fills itself (tsb_peer_store_alloc) without a model file on disk.
 __global__ void fill_bytes_kernel(uint64_t file_id, uint64_t first, uint64_t n, uint8_t* __restrict__ dst) {
@@ -207,19 +232,49 @@ __global__ void fill_bytes_kernel(uint64_t file_id, uint64_t first, uint64_t n, 
   for (uint64_t j = (uint64_t(blockIdx.x) * blockDim.x + threadIdx.x) * 8; j < n; j += stride) {
     uint64_t word = 0;
     const uint64_t m = n - j < 8 ? n - j : 8;
-    for (uint64_t k = 0; k < m; ++k) {
-      const uint64_t i = first + j + k;
-      uint64_t x = (i + 1) * 0x9E3779B97F4A7C15ULL ^ (file_id + 7) * 0xC2B2AE3D27D4EB4FULL;
-      x ^= x >> 29;
-      x *= 0xBF58476D1CE4E5B9ULL;
-      x ^= x >> 32;
-      word |= uint64_t(uint8_t(x)) << (8 * k);
-    }
+    for (uint64_t k = 0; k < m; ++k) word |= uint64_t(gen_byte(file_id, first + j + k)) << (8 * k);
     if (m == 8 && ((reinterpret_cast<uintptr_t>(dst + j) & 7u) == 0)) {
       *reinterpret_cast<uint64_t*>(dst + j) = word;
     } else {
       for (uint64_t k = 0; k < m; ++k) dst[j + k] = uint8_t(word >> (8 * k));
     }
+  }
+}
+
+// The reader's checksum of unit i (unit_bytes from file position offsets[i]) computed from the byte generator alone,
+// never from a copy: grid (n, slices), each block a slice of the unit's 16-byte groups, in reader_kernel's modes
+// (0: sum(byte x (pos % 251 + 1)), 1: the sum of the unit's 32-bit little-endian words). unit_bytes % 16 == 0.
+__global__ __launch_bounds__(kThreads) void expect_sums_kernel(uint64_t file_id, const uint64_t* offsets,
+                                                               uint64_t unit_bytes, int mode,
+                                                               unsigned long long* out) {
+  const uint32_t i = blockIdx.x;
+  const uint64_t base = offsets[i];
+  const uint64_t n16 = unit_bytes / 16;
+  const uint64_t per = (n16 + gridDim.y - 1) / gridDim.y;
+  const uint64_t lo = per * blockIdx.y, hi = lo + per < n16 ? lo + per : n16;
+  uint64_t acc = 0;
+  for (uint64_t e = lo + threadIdx.x; e < hi; e += kThreads) {
+    const uint64_t pos = e * 16;
+    uint32_t m = uint32_t(pos % 251);
+#pragma unroll
+    for (int k = 0; k < 16; ++k) {
+      const uint64_t b = gen_byte(file_id, base + pos + uint64_t(k));
+      if (mode == 1) {
+        acc += b << (8 * (k & 3));
+      } else {
+        acc += b * (m + 1);
+        m = m + 1 == 251 ? 0 : m + 1;
+      }
+    }
+  }
+  __shared__ uint64_t part[kThreads / 32];
+  acc = warp_sum(acc);
+  if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = acc;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    uint64_t s = 0;
+    for (int k = 0; k < kThreads / 32; ++k) s += part[k];
+    atomicAdd(out + i, (unsigned long long)s);
   }
 }
 
@@ -233,6 +288,19 @@ __attribute__((visibility("default"))) int tse_fill_units_device(uint64_t file_i
     if (e != cudaSuccess) return int(e);
   }
   return 0;
+}
+
+// Expected reader checksums of n units from the generator (expect_sums_kernel): offsets_dev[n] (device) the units'
+// file positions, out_dev[n] (device) zeroed here first, on `stream`.
+__attribute__((visibility("default"))) int tse_expect_sums(uint64_t file_id, const uint64_t* offsets_dev, uint32_t n,
+                                                           uint64_t unit_bytes, int mode, unsigned long long* out_dev,
+                                                           uint32_t slices, void* stream) {
+  if (!n) return 0;
+  if (unit_bytes % 16 != 0 || (mode != 0 && mode != 1)) return int(cudaErrorInvalidValue);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  CK(cudaMemsetAsync(out_dev, 0, size_t(n) * 8, s));
+  expect_sums_kernel<<<dim3(n, slices ? slices : 1), kThreads, 0, s>>>(file_id, offsets_dev, unit_bytes, mode, out_dev);
+  return int(cudaGetLastError());
 }
 
 __attribute__((visibility("default"))) int tse_launch(void* exec, void* stream) {

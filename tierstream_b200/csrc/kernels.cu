@@ -95,28 +95,68 @@ __global__ __launch_bounds__(kCopyThreads) void batch_kernel(const __grid_consta
 }
 
 // ---------------------------------------------------------------------------------------------------------------
-// K3: xxh64 of whole units. XXH64 is four serial lane chains per unit (one 64-bit multiply-rotate-multiply per 32-byte
-// stripe and lane), so a unit's rate is set by that chain's latency and the kernel's job is to keep the chain fed and
-// run many chains at once. A CTA is one warp serving 16 units: thread t carries accumulator (t & 3) of units t >> 2
-// and (t >> 2) + 8, two independent chains interleaved. Bytes are staged in shared memory by TMA bulk copies (one
-// cp.async.bulk per unit and chunk, issued by the unit's own lane, completing on the chunk's mbarrier) through a
-// ring of 4 x 2 KiB stages per unit; unit buffers are offset by 32 B in rotation so a quad's 32-byte reads of eight
-// units spread over the banks. Units whose spans are not 16-byte aligned, or not 32-byte multiples except the last,
-// take a one-lane path from global memory. Every mbarrier wait is bounded (2 s of globaltimer, or an iteration cap);
-// one that runs out counts in g_xxh64_timeouts, marks the CTA's units as mismatches and returns after a bounded wait
-// for the copies it already issued.
+// K3: xxh64 of whole units. XXH64 is four serial lane chains per unit (a 64-bit add, rotate and multiply per 32-byte
+// stripe and lane), so one unit's rate is set by the latency of that chain; the kernel keeps each chain as short as
+// the arithmetic allows and runs many units at once. A CTA is two independent warps; a warp serves 8 units, thread t
+// carrying accumulator t & 3 of unit t >> 2. The input product x * P2 of eight stripes is computed ahead of their
+// steps, so the chain itself is an add with carry, two funnel shifts and one widening multiply with its two cross
+// products. Bytes are staged in shared memory by TMA bulk copies (one cp.async.bulk per unit, chunk and span, issued
+// by the unit's own lane, completing on the warp's mbarrier of that stage) through a ring of 4 x 2 KiB stages per
+// unit; unit rings are offset by 32 B in rotation so a half-warp's 32-byte reads of four units fall in distinct banks.
+// Units whose spans are not 16-byte aligned, or not 32-byte multiples except the last, take a one-lane path from
+// global memory. Every mbarrier wait is bounded (2 s of globaltimer, or an iteration cap); one that runs out is
+// counted in the launch's timeout word, reports the warp's units as failed (hash 0) and returns after a bounded wait
+// for the copies already issued.
 // ---------------------------------------------------------------------------------------------------------------
 constexpr uint64_t X1 = 0x9E3779B185EBCA87ULL, X2 = 0xC2B2AE3D27D4EB4FULL, X3 = 0x165667B19E3779F9ULL,
                    X4 = 0x85EBCA77C2B2AE63ULL, X5 = 0x27D4EB2F165667C5ULL;
-constexpr int kHashUnits = 16, kHashStages = 4, kHashChunk = 2048;
+constexpr uint32_t kX1lo = uint32_t(X1), kX1hi = uint32_t(X1 >> 32);
+constexpr int kHashWarpUnits = 8, kHashWarps = 2, kHashUnits = kHashWarpUnits * kHashWarps;
+constexpr int kHashStages = 4, kHashChunk = 2048;
 constexpr int kHashRegion = kHashStages * kHashChunk + 128;  // one unit's ring, plus room for the bank offset
-constexpr size_t kHashSmem = size_t(kHashUnits) * kHashRegion + kHashStages * 8;
+constexpr size_t kHashWarpBytes = size_t(kHashWarpUnits) * kHashRegion;
+constexpr size_t kHashSmem = size_t(kHashWarps) * kHashWarpBytes + size_t(kHashWarps) * kHashStages * 8;
 constexpr unsigned long long kWaitNs = 2000000000ull;
 
 __device__ uint32_t g_xxh64_timeouts;
 
 __device__ __forceinline__ uint64_t rotl64(uint64_t v, uint32_t r) { return (v << r) | (v >> (64 - r)); }
 __device__ __forceinline__ uint64_t lane_step(uint64_t acc, uint64_t w) { return rotl64(acc + w * X2, 31) * X1; }
+
+// One stripe step of a lane chain, acc = rotl(acc + y, 31) * P1 with y = x * P2 already computed: the add with carry,
+// the rotation as two funnel shifts ({hi:lo} << 31 | {hi:lo} >> 33), the product mod 2^64 as lo x P1lo widened plus
+// the two cross products into the high word.
+__device__ __forceinline__ void chain_step(uint32_t& lo, uint32_t& hi, uint64_t y) {
+  uint32_t rl, rh;
+  asm("{\n\t.reg .u32 tl, th;\n\t"
+      "add.cc.u32 tl, %2, %4;\n\t"
+      "addc.u32 th, %3, %5;\n\t"
+      "shf.l.wrap.b32 %0, th, tl, 31;\n\t"
+      "shf.l.wrap.b32 %1, tl, th, 31;\n\t"
+      "}"
+      : "=r"(rl), "=r"(rh)
+      : "r"(lo), "r"(hi), "r"(uint32_t(y)), "r"(uint32_t(y >> 32)));
+  const uint64_t d = uint64_t(rl) * kX1lo;
+  lo = uint32_t(d);
+  hi = uint32_t(d >> 32) + rl * kX1hi + rh * kX1lo;
+}
+// n (1..64) stripes of this thread's lane (its word every 32 bytes from w) into acc; the input products eight ahead.
+__device__ __forceinline__ uint64_t chain_stripes(uint64_t acc, const uint64_t* w, uint32_t n) {
+  uint32_t lo = uint32_t(acc), hi = uint32_t(acc >> 32);
+  if (n == kHashChunk / 32) {
+#pragma unroll 2
+    for (int g = 0; g < kHashChunk / 32; g += 8) {
+      uint64_t y[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) y[k] = w[4 * (g + k)] * X2;
+#pragma unroll
+      for (int k = 0; k < 8; ++k) chain_step(lo, hi, y[k]);
+    }
+  } else {
+    for (uint32_t s = 0; s < n; ++s) chain_step(lo, hi, w[4 * s] * X2);
+  }
+  return uint64_t(hi) << 32 | lo;
+}
 
 __device__ __forceinline__ unsigned long long globaltimer_ns() {
   unsigned long long t;
@@ -203,19 +243,64 @@ __device__ __forceinline__ uint64_t seed_acc(uint32_t l) {  // seed 0
   return l == 0 ? X1 + X2 : l == 1 ? X2 : l == 2 ? 0 : uint64_t(0) - X1;
 }
 
-__global__ __launch_bounds__(32) void xxh64_kernel(const HashUnit* __restrict__ units, uint32_t n,
-                                                   const uint64_t* __restrict__ expect, uint64_t* __restrict__ out,
-                                                   uint32_t* __restrict__ bad, uint32_t* __restrict__ mismatches) {
-  extern __shared__ __align__(128) uint8_t smem[];
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + size_t(kHashUnits) * kHashRegion);
-  const uint32_t lane = threadIdx.x, q = lane >> 2, l = lane & 3;
-  const uint32_t first = blockIdx.x * kHashUnits;
-  // lane i < 16 holds unit first + i: its spans, whether it takes the staged path, its staged (stripe) bytes
+// Where a launch's units come from and where their hashes go. A table in device memory (tsb_xxh64_units and the
+// open's checks): out[i] = the hash; with expectations, a mismatch (or a failed unit) sets bad[i] and adds 1 to
+// *mismatches.
+struct TableUnits {
+  const HashUnit* units;
+  const uint64_t* expect;
+  uint64_t* out;
+  uint32_t* bad;
+  uint32_t* mismatches;
+  __device__ HashUnit unit(uint32_t i) const { return units[i]; }
+  __device__ void result(uint32_t i, uint64_t h, bool failed) const {
+    out[i] = h;
+    if (failed || (expect && expect[i] != h)) {
+      if (bad) bad[i] = 1;
+      if (expect && mismatches) atomicAdd(mismatches, 1u);
+    }
+  }
+};
+// Landed slots of a device-gated arena, by value in the launch: unit i is key[i] in slot[i]; compared with
+// expect[key]. A mismatch adds 1 to *bad_count and, while the log has room, writes (key, slot) to the mapped log.
+struct LandedUnits {
+  const VerifyBatch* b;
+  __device__ HashUnit unit(uint32_t i) const {
+    HashUnit u{};
+    u.n_spans = b->n_parts;
+    const uint64_t slot = uint64_t(uint32_t(b->slot[i]));
+    for (uint32_t p = 0; p < b->n_parts && p < 4; ++p) {
+      u.span[p] = b->arena[p] + slot * b->part_bytes[p];
+      u.bytes[p] = b->part_bytes[p];
+    }
+    return u;
+  }
+  __device__ void result(uint32_t i, uint64_t h, bool failed) const {
+    if (!failed && b->expect[b->key[i]] == h) return;
+    const uint32_t at = atomicAdd(b->bad_count, 1u);
+    if (at < kBadLog) {
+      volatile uint32_t* log = b->bad_log;
+      log[2 * at] = b->key[i];
+      log[2 * at + 1] = uint32_t(b->slot[i]);
+    }
+    __threadfence_system();  // the entry before the flag
+    *reinterpret_cast<volatile uint32_t*>(b->bad_flag) = 1u;
+    __threadfence_system();
+  }
+};
+
+// One warp's 8 units (first .. first + 7) through its region of shared memory and its stage barriers.
+template <class Src>
+__device__ void hash_warp(const Src& src, uint32_t n, uint32_t first, uint8_t* wsmem, uint64_t* bars,
+                          uint32_t* timeouts) {
+  const uint32_t lane = threadIdx.x & 31u, q = lane >> 2, l = lane & 3u;
+  // lane i < 8 holds unit first + i: its spans, whether it takes the staged path, its staged (stripe) bytes
   HashUnit mine{};
-  uint64_t body = 0, total = 0;
-  if (lane < kHashUnits && first + lane < n) {
-    mine = units[first + lane];
+  uint64_t body = 0;
+  if (lane < uint32_t(kHashWarpUnits) && first + lane < n) {
+    mine = src.unit(first + lane);
     bool ok = mine.n_spans >= 1 && mine.n_spans <= 4;
+    uint64_t total = 0;
 #pragma unroll
     for (uint32_t s = 0; s < 4; ++s) {
       if (s >= mine.n_spans) break;
@@ -225,14 +310,11 @@ __global__ __launch_bounds__(32) void xxh64_kernel(const HashUnit* __restrict__ 
     }
     body = ok ? total / 32 * 32 : 0;
   }
-  const uint32_t my_chunks = uint32_t((body + kHashChunk - 1) / kHashChunk);
-  const uint32_t nchunks = __reduce_max_sync(0xffffffffu, my_chunks);
-  // the two units this thread hashes: q and q + 8
-  const uint64_t body0 = __shfl_sync(0xffffffffu, body, int(q)), body1 = __shfl_sync(0xffffffffu, body, int(q + 8));
-  uint8_t* region = smem + size_t(lane) * kHashRegion + (lane & 3u) * 32;  // valid for lane < 16
-  const uint8_t* rd0 = smem + size_t(q) * kHashRegion + (q & 3u) * 32 + 8 * l;
-  const uint8_t* rd1 = smem + size_t(q + 8) * kHashRegion + ((q + 8) & 3u) * 32 + 8 * l;
-  if (lane == 0) {
+  const uint32_t nchunks = __reduce_max_sync(0xffffffffu, uint32_t((body + kHashChunk - 1) / kHashChunk));
+  const uint64_t body_q = __shfl_sync(0xffffffffu, body, int(q));
+  uint8_t* region = wsmem + size_t(lane) * kHashRegion + (lane & 3u) * 32;  // valid for lane < 8
+  const uint8_t* rd = wsmem + size_t(q) * kHashRegion + (q & 3u) * 32 + 8 * l;
+  if (lane == 0 && nchunks) {
     for (int s = 0; s < kHashStages; ++s) mbar_init(bars + s, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -266,8 +348,8 @@ __global__ __launch_bounds__(32) void xxh64_kernel(const HashUnit* __restrict__ 
       p = 0;
     }
   };
-  for (uint32_t c = 0; c < kHashStages && c < nchunks; ++c) issue(c);
-  uint64_t a0 = seed_acc(l), a1 = seed_acc(l);
+  for (uint32_t c = 0; c < uint32_t(kHashStages) && c < nchunks; ++c) issue(c);
+  uint64_t acc = seed_acc(l);
   bool timed_out = false;
   uint32_t c = 0;
   for (; c < nchunks; ++c) {
@@ -276,69 +358,67 @@ __global__ __launch_bounds__(32) void xxh64_kernel(const HashUnit* __restrict__ 
       timed_out = true;
       break;
     }
-    const size_t so = size_t(c % kHashStages) * kHashChunk;
-    const uint64_t* w0 = reinterpret_cast<const uint64_t*>(rd0 + so);
-    const uint64_t* w1 = reinterpret_cast<const uint64_t*>(rd1 + so);
+    const uint64_t* w = reinterpret_cast<const uint64_t*>(rd + size_t(c % kHashStages) * kHashChunk);
     const uint64_t start = uint64_t(c) * kHashChunk;
-    const uint32_t n0 = start < body0 ? uint32_t((body0 - start < kHashChunk ? body0 - start : kHashChunk) / 32) : 0u;
-    const uint32_t n1 = start < body1 ? uint32_t((body1 - start < kHashChunk ? body1 - start : kHashChunk) / 32) : 0u;
-    // the two chains' steps interleaved: each step waits only on its own chain
-    if (n0 == kHashChunk / 32 && n1 == kHashChunk / 32) {
-#pragma unroll 16
-      for (int s = 0; s < kHashChunk / 32; ++s) {
-        a0 = lane_step(a0, w0[4 * s]);
-        a1 = lane_step(a1, w1[4 * s]);
-      }
-    } else {
-      for (uint32_t s = 0; s < n0; ++s) a0 = lane_step(a0, w0[4 * s]);
-      for (uint32_t s = 0; s < n1; ++s) a1 = lane_step(a1, w1[4 * s]);
-    }
+    const uint32_t nq = start < body_q ? uint32_t((body_q - start < kHashChunk ? body_q - start : kHashChunk) / 32) : 0u;
+    if (nq) acc = chain_stripes(acc, w, nq);
     __syncwarp();  // every lane is done with the stage before it is refilled
     if (c + kHashStages < nchunks) issue(c + kHashStages);
   }
   if (timed_out) {
-    if (lane == 0) atomicAdd(&g_xxh64_timeouts, 1u);
-    // the copies already issued (stages c .. c + kHashStages - 1) land before the CTA leaves, each wait bounded
+    if (lane == 0) atomicAdd(timeouts ? timeouts : &g_xxh64_timeouts, 1u);
+    // the copies already issued (stages c .. c + kHashStages - 1) land before the warp leaves, each wait bounded
     for (uint32_t k = c; k < nchunks && k < c + kHashStages; ++k)
       (void)mbar_wait(bars + (k % kHashStages), (k / kHashStages) & 1u);
-    if (lane < kHashUnits && first + lane < n) {
-      out[first + lane] = 0;
-      if (bad) bad[first + lane] = 1;
-      if (expect && mismatches) atomicAdd(mismatches, 1u);
-    }
+    if (lane < uint32_t(kHashWarpUnits) && first + lane < n) src.result(first + lane, 0, true);
     return;
   }
-  // gather each quad's accumulators on its lane 0, then finish units q and q + 8 there
-  uint64_t v0[4], v1[4];
+  // each quad's accumulators on its lane 0, which finishes unit first + q
+  uint64_t v[4];
 #pragma unroll
-  for (int k = 0; k < 4; ++k) {
-    v0[k] = __shfl_sync(0xffffffffu, a0, int((lane & ~3u) + k));
-    v1[k] = __shfl_sync(0xffffffffu, a1, int((lane & ~3u) + k));
+  for (int k = 0; k < 4; ++k) v[k] = __shfl_sync(0xffffffffu, acc, int((lane & ~3u) + k));
+  const uint32_t idx = first + q;
+  if (l != 0 || idx >= n) return;
+  const HashUnit u = src.unit(idx);
+  uint64_t t = 0;
+  for (uint32_t s = 0; s < u.n_spans && s < 4; ++s) t += u.bytes[s];
+  uint64_t h;
+  if (body_q) {
+    h = finish_hash(u, v, t, body_q);
+  } else {  // shorter than a stripe, or the one-lane path from global memory
+    uint64_t a[4] = {seed_acc(0), seed_acc(1), seed_acc(2), seed_acc(3)};
+    const uint64_t bb = t / 32 * 32;
+    for (uint64_t p = 0; p < bb; p += 32)
+      for (int k = 0; k < 4; ++k) a[k] = lane_step(a[k], unit_le64(u, p + 8 * uint64_t(k)));
+    h = finish_hash(u, a, t, bb);
   }
-  if (l != 0) return;
-  for (int which = 0; which < 2; ++which) {
-    const uint32_t idx = first + q + 8u * uint32_t(which);
-    if (idx >= n) continue;
-    const HashUnit& u = units[idx];
-    const uint64_t b = which ? body1 : body0;
-    uint64_t t = 0;
-    for (uint32_t s = 0; s < u.n_spans && s < 4; ++s) t += u.bytes[s];
-    uint64_t h;
-    if (b) {
-      h = finish_hash(u, which ? v1 : v0, t, b);
-    } else {  // shorter than a stripe, or the one-lane path from global memory
-      uint64_t a[4] = {seed_acc(0), seed_acc(1), seed_acc(2), seed_acc(3)};
-      const uint64_t bb = t / 32 * 32;
-      for (uint64_t p = 0; p < bb; p += 32)
-        for (int k = 0; k < 4; ++k) a[k] = lane_step(a[k], unit_le64(u, p + 8 * uint64_t(k)));
-      h = finish_hash(u, a, t, bb);
-    }
-    out[idx] = h;
-    if (expect && expect[idx] != h) {
-      if (bad) bad[idx] = 1;
-      if (mismatches) atomicAdd(mismatches, 1u);
-    }
-  }
+  src.result(idx, h, false);
+}
+
+__global__ __launch_bounds__(32 * kHashWarps) void xxh64_kernel(const HashUnit* __restrict__ units, uint32_t n,
+                                                                const uint64_t* __restrict__ expect,
+                                                                uint64_t* __restrict__ out, uint32_t* __restrict__ bad,
+                                                                uint32_t* __restrict__ mismatches, uint32_t* timeouts) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  const uint32_t w = threadIdx.x >> 5;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kHashWarps * kHashWarpBytes) + w * kHashStages;
+  const TableUnits src{units, expect, out, bad, mismatches};
+  hash_warp(src, n, (blockIdx.x * kHashWarps + w) * kHashWarpUnits, smem + w * kHashWarpBytes, bars, timeouts);
+}
+
+__global__ __launch_bounds__(32 * kHashWarps) void xxh64_landed_kernel(const __grid_constant__ VerifyBatch b) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  const uint32_t w = threadIdx.x >> 5;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kHashWarps * kHashWarpBytes) + w * kHashStages;
+  const LandedUnits src{&b};
+  hash_warp(src, b.n, (blockIdx.x * kHashWarps + w) * kHashWarpUnits, smem + w * kHashWarpBytes, bars, b.timeouts);
+  __syncthreads();
+  if (threadIdx.x != 0) return;
+  __threadfence_system();  // this CTA's log entries before the launch's done word
+  if (atomicAdd(b.done_cnt, 1u) != gridDim.x - 1) return;
+  *reinterpret_cast<volatile uint32_t*>(b.done_cnt) = 0u;
+  __threadfence_system();
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(b.done_word), "r"(b.done_val) : "memory");
 }
 
 // ---------------------------------------------------------------------------------------------------------------
@@ -573,6 +653,21 @@ __global__ void dg_end_kernel(DgDev d) {
 
 int last_error() { return int(cudaGetLastError()); }
 
+// A kernel's dynamic shared memory limit is a per-device setting: raised once on each device (bit d of `done`), by
+// whichever thread gets there first (setting it twice is harmless).
+template <typename K>
+int raise_smem_once(K kernel, size_t bytes, std::atomic<uint64_t>& done) {
+  int device = 0;
+  if (const cudaError_t e = cudaGetDevice(&device); e != cudaSuccess) return int(e);
+  const uint64_t bit = device >= 0 && device < 64 ? uint64_t(1) << device : 0;
+  if (bit && (done.load(std::memory_order_acquire) & bit)) return 0;
+  const cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(bytes));
+  if (e != cudaSuccess) return int(e);
+  done.fetch_or(bit, std::memory_order_acq_rel);
+  return 0;
+}
+std::atomic<uint64_t> g_move_smem_set{0}, g_xxh64_smem_set{0}, g_landed_smem_set{0};
+
 }  // namespace
 
 int launch_batch(const Batch& b, int blocks, void* stream) {
@@ -592,16 +687,7 @@ bool move_fits(const Batch& b) {
 
 int launch_move(const Batch& b, int blocks, void* stream) {
   if (b.n_copies > kMaxCopies || b.n_entries > kMaxEntries || !move_fits(b)) return int(cudaErrorInvalidValue);
-  // the shared-memory attribute is a per-device setting of the kernel
-  static std::atomic<uint64_t> set_on{0};
-  int device = 0;
-  if (const cudaError_t e = cudaGetDevice(&device); e != cudaSuccess) return int(e);
-  const uint64_t bit = device < 64 ? uint64_t(1) << device : 0;
-  if (!bit || !(set_on.load() & bit)) {
-    const cudaError_t e = cudaFuncSetAttribute(move_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kMoveSmem));
-    if (e != cudaSuccess) return int(e);
-    set_on.fetch_or(bit);
-  }
+  if (const int e = raise_smem_once(move_kernel, kMoveSmem, g_move_smem_set)) return e;
   if (blocks < 1) blocks = 1;
   move_kernel<<<blocks, 32, kMoveSmem, static_cast<cudaStream_t>(stream)>>>(b);
   return last_error();
@@ -619,18 +705,23 @@ int move_take_timeouts(uint32_t* out) {
 }
 
 int launch_xxh64(const HashUnit* units_dev, uint32_t n, const uint64_t* expect_dev, uint64_t* out_dev,
-                 uint32_t* bad_dev, uint32_t* mismatches_dev, void* stream) {
+                 uint32_t* bad_dev, uint32_t* mismatches_dev, void* stream, uint32_t* timeouts_dev) {
   if (!n) return 0;
-  static bool attr = false;
-  if (!attr) {
-    const cudaError_t e =
-        cudaFuncSetAttribute(xxh64_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kHashSmem));
-    if (e != cudaSuccess) return int(e);
-    attr = true;
-  }
+  if (const int e = raise_smem_once(xxh64_kernel, kHashSmem, g_xxh64_smem_set)) return e;
   const uint32_t blocks = (n + kHashUnits - 1) / kHashUnits;
-  xxh64_kernel<<<blocks, 32, kHashSmem, static_cast<cudaStream_t>(stream)>>>(units_dev, n, expect_dev, out_dev,
-                                                                             bad_dev, mismatches_dev);
+  xxh64_kernel<<<blocks, 32 * kHashWarps, kHashSmem, static_cast<cudaStream_t>(stream)>>>(
+      units_dev, n, expect_dev, out_dev, bad_dev, mismatches_dev, timeouts_dev);
+  return last_error();
+}
+
+int launch_xxh64_landed(const VerifyBatch& b, void* stream) {
+  if (!b.n) return 0;
+  if (b.n > kMaxVerify || b.n_parts < 1 || b.n_parts > 4 || !b.expect || !b.bad_count || !b.bad_log ||
+      !b.bad_flag || !b.timeouts || !b.done_cnt || !b.done_word)
+    return int(cudaErrorInvalidValue);
+  if (const int e = raise_smem_once(xxh64_landed_kernel, kHashSmem, g_landed_smem_set)) return e;
+  const uint32_t blocks = (b.n + kHashUnits - 1) / kHashUnits;
+  xxh64_landed_kernel<<<blocks, 32 * kHashWarps, kHashSmem, static_cast<cudaStream_t>(stream)>>>(b);
   return last_error();
 }
 
@@ -657,14 +748,16 @@ int launch_dg_end(const DgDev& d, void* s) {
 
 int preload() {
   cudaFuncAttributes a;
-  const void* fns[] = {(const void*)batch_kernel,     (const void*)xxh64_kernel,      (const void*)dg_begin_kernel,
-                       (const void*)dg_export_kernel, (const void*)dg_predict_kernel, (const void*)dg_wait_kernel,
-                       (const void*)dg_end_kernel};
+  const void* fns[] = {(const void*)batch_kernel,      (const void*)xxh64_kernel,     (const void*)xxh64_landed_kernel,
+                       (const void*)move_kernel,       (const void*)dg_begin_kernel,  (const void*)dg_export_kernel,
+                       (const void*)dg_predict_kernel, (const void*)dg_wait_kernel,   (const void*)dg_end_kernel};
   for (const void* f : fns) {
     const cudaError_t e = cudaFuncGetAttributes(&a, f);
     if (e != cudaSuccess) return int(e);
   }
-  return int(cudaFuncSetAttribute(xxh64_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kHashSmem)));
+  if (const int e = raise_smem_once(xxh64_kernel, kHashSmem, g_xxh64_smem_set)) return e;
+  if (const int e = raise_smem_once(xxh64_landed_kernel, kHashSmem, g_landed_smem_set)) return e;
+  return raise_smem_once(move_kernel, kMoveSmem, g_move_smem_set);
 }
 
 int xxh64_take_timeouts(uint32_t* out) {

@@ -40,7 +40,9 @@ int move_take_timeouts(uint32_t* out);
 
 // ---- K3: device xxh64 of whole units ----
 // A unit is up to 4 spans hashed back to back (a gated unit's parts in the arena). out[i] = the hash; when expect is
-// given, a mismatch increments *mismatches and sets bad[i] = 1 (bad may be null).
+// given, a mismatch increments *mismatches and sets bad[i] = 1 (bad may be null). timeouts_dev: the word counting
+// staging waits that ran out (null: this library's per-device word, read by xxh64_take_timeouts); a failed unit is
+// hashed as 0 and reported as a mismatch.
 struct HashUnit {
   const uint8_t* span[4];
   uint64_t bytes[4];
@@ -48,10 +50,34 @@ struct HashUnit {
   uint32_t pad;
 };
 int launch_xxh64(const HashUnit* units_dev, uint32_t n, const uint64_t* expect_dev, uint64_t* out_dev,
-                 uint32_t* bad_dev, uint32_t* mismatches_dev, void* stream);
-// Staging waits of the xxh64 kernel that ran out since the last call (their units were reported as mismatches and
-// hashed as 0), then reset; synchronous. Non-zero means the device did not complete a bulk copy in 2 s.
+                 uint32_t* bad_dev, uint32_t* mismatches_dev, void* stream, uint32_t* timeouts_dev = nullptr);
+// Staging waits of the xxh64 kernel that ran out since the last call on this device (launches given no timeout word),
+// then reset; synchronous. Non-zero means the device did not complete a bulk copy in 2 s.
 int xxh64_take_timeouts(uint32_t* out);
+// K3 over landed slots of a device-gated arena (the landing check), passed by value in the launch: unit i is key[i]
+// in slot[i] (part p at arena[p] + slot x part_bytes[p]), compared with expect[key]. A mismatch (or a unit whose
+// staging wait ran out, counted in *timeouts) adds 1 to *bad_count, writes (key, slot) at bad_log[2 x its index] while
+// the log has room (kBadLog entries), then *bad_flag = 1; bad_log and bad_flag are mapped host memory, written with
+// system-scope stores so the host reads them without a device call. When every CTA of the launch finished, its last
+// one resets *done_cnt and stores done_val to *done_word (mapped, release at system scope): the host learns of a
+// finished launch without recording an event after it.
+constexpr uint32_t kMaxVerify = 256, kBadLog = 64;
+struct VerifyBatch {
+  const uint8_t* arena[4];
+  uint64_t part_bytes[4];
+  uint32_t n_parts, n;
+  const uint64_t* expect;  // [keys], device
+  uint32_t* bad_count;     // device
+  uint32_t* bad_log;       // mapped host, 2 x kBadLog words
+  uint32_t* bad_flag;      // mapped host
+  uint32_t* timeouts;      // device
+  uint32_t* done_cnt;      // device, zero before the launch
+  uint32_t* done_word;     // mapped host
+  uint32_t done_val, pad;
+  uint32_t key[kMaxVerify];
+  int32_t slot[kMaxVerify];
+};
+int launch_xxh64_landed(const VerifyBatch& b, void* stream);
 
 // ---- K2: device-gated decode control kernels ----
 // The record an export writes for the service (mapped host memory); the layout is the reference's DgRecord

@@ -93,14 +93,29 @@ class DgRun:
         self.pred_dev = torch.zeros(max(1, G * n_pred), dtype=torch.int32, device="cuda")
         self.out_dev = torch.zeros(G * max_ids, dtype=torch.int64, device="cuda")
         self.out_pin = torch.zeros(G * max_ids, dtype=torch.int64).pin_memory()
+        self.stream.wait_stream(torch.cuda.current_stream())  # the zero fills above ran on torch's stream
         self.graph = runtime.TokenGraph(self.ctx, G, self.ids_dev.data_ptr(), max_ids, self.out_dev.data_ptr(),
                                         self.stream.cuda_stream, slices=slices, mode=mode,
                                         pred_dev=self.pred_dev.data_ptr() if n_pred else 0, n_pred=n_pred,
                                         with_reader=with_reader)
         self.keys = G * U
+        self.graphs = {mode: self.graph}
+        self._graph_args = dict(slices=slices, pred_dev=self.pred_dev.data_ptr() if n_pred else 0, n_pred=n_pred,
+                                with_reader=with_reader)
 
-    def step(self, ids, preds=None, sync=True):
-        """One token: routed ids [G][max_ids] (and predictions [G][n_pred]); returns the readers' checksums."""
+    def graph_for(self, mode):
+        """The token graph whose readers check in `mode` (0: positional checksum, 1: word sum), captured on first use
+        on the same context, buffers and stream."""
+        if mode not in self.graphs:
+            self.graphs[mode] = runtime.TokenGraph(self.ctx, self.G, self.ids_dev.data_ptr(), self.n_ids,
+                                                   self.out_dev.data_ptr(), self.stream.cuda_stream, mode=mode,
+                                                   **self._graph_args)
+        return self.graphs[mode]
+
+    def step(self, ids, preds=None, sync=True, mode=None):
+        """One token: routed ids [G][max_ids] (and predictions [G][n_pred]); returns the readers' checksums (in `mode`,
+        default the graph's of the open)."""
+        graph = self.graph if mode is None else self.graph_for(mode)
         self.ids_pin.numpy()[:] = np.asarray(ids, dtype=np.int32).reshape(-1)
         if preds is not None:
             self.pred_pin.numpy()[:self.G * self.n_pred] = np.asarray(preds, dtype=np.int32).reshape(-1)
@@ -109,7 +124,7 @@ class DgRun:
             self.ids_dev.copy_(self.ids_pin, non_blocking=True)
             if preds is not None:
                 self.pred_dev.copy_(self.pred_pin, non_blocking=True)
-            self.graph.launch()
+            graph.launch()
             self.out_pin.copy_(self.out_dev, non_blocking=True)
         if sync:
             self.stream.synchronize()
@@ -117,6 +132,9 @@ class DgRun:
         return self.out_pin.numpy().reshape(self.G, self.n_ids).astype(np.uint64)
 
     def close(self):
+        for g in getattr(self, "graphs", {}).values():
+            g.close()
+        self.graphs = {}
         if getattr(self, "graph", None):
             self.graph.close()
         if getattr(self, "ctx", None):
@@ -128,3 +146,33 @@ def model_dir():
         if os.path.isdir(d) and os.access(d, os.W_OK):
             return d
     return "."
+
+
+def expected_sums(model, keys, mode, slices=64):
+    """The reader's checksum of each unit keys[i] (key = layer x units + unit), computed on the current device from
+    the model's byte generator alone (libtsb_engine.so tse_expect_sums: no copy the runtime made is read); uint64."""
+    keys = np.asarray(keys, dtype=np.int64).reshape(-1)
+    out = np.zeros(keys.size, dtype=np.uint64)
+    if not keys.size:
+        return out
+    offs = np.array([model.unit_offset(int(k) // model.units, int(k) % model.units) for k in keys], dtype=np.uint64)
+    offs_dev = torch.from_numpy(offs.view(np.int64)).cuda()
+    res = torch.zeros(keys.size, dtype=torch.int64, device="cuda")
+    s = torch.cuda.current_stream()
+    rc = abi.load_engine().tse_expect_sums(model.seed, offs_dev.data_ptr(), keys.size, model.unit_bytes, mode,
+                                           res.data_ptr(), slices, s.cuda_stream)
+    if rc != 0:
+        raise RuntimeError("tse_expect_sums failed: %d" % rc)
+    out[:] = res.cpu().numpy().view(np.uint64)
+    return out
+
+
+def check_reads(outs, ids, units, want):
+    """Compares reader outputs outs[t][g][k] with want[key] for key = g x units + ids[t][g][k]: (units checked,
+    mismatches, the first mismatch as (token, layer, k) or None)."""
+    outs = np.asarray(outs, dtype=np.uint64)
+    ids = np.asarray(ids, dtype=np.int64)
+    keys = np.arange(ids.shape[1])[None, :, None] * units + ids
+    bad = outs != want[keys]
+    first = tuple(int(x) for x in np.argwhere(bad)[0]) if bad.any() else None
+    return int(bad.size), int(bad.sum()), first

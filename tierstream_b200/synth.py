@@ -66,16 +66,45 @@ class Model:
                                          out.ctypes.data, 4)
         return out
 
-    def hashes(self):
-        """xxh64 of every unit (layer-major), by the library's host xxh64."""
-        if self._hashes is None:
-            lib = abi.load()
+    def hashes(self, threads=None):
+        """xxh64 of every unit (layer-major), by the library's host xxh64: from the model file when it is written (a
+        pool of threads, each reading and hashing whole units; the result is kept beside the file as <path>.xxh64 and
+        reused while it is newer than the file), else from the byte generator."""
+        if self._hashes is not None:
+            return self._hashes
+        n = self.layers * self.units
+        lib = abi.load()
+        side = self.path + ".xxh64"
+        written = os.path.exists(self.path) and os.path.getsize(self.path) == self.file_bytes
+        if written and os.path.exists(side) and os.path.getsize(side) == 8 * n and \
+                os.path.getmtime(side) >= os.path.getmtime(self.path):
+            self._hashes = [int(x) for x in np.fromfile(side, dtype=np.uint64)]
+            return self._hashes
+        if not written:
             h = []
             for L in range(self.layers):
                 for u in range(self.units):
                     b = self.unit_bytes_of(L, u)
                     h.append(int(lib.tsb_xxh64(b.ctypes.data, b.size, 0)))
             self._hashes = h
+            return h
+        from concurrent.futures import ThreadPoolExecutor
+        out = np.zeros(n, dtype=np.uint64)
+
+        def one(k):
+            buf = np.empty(self.unit_bytes, dtype=np.uint8)
+            with open(self.path, "rb", buffering=0) as f:
+                f.seek(self.unit_offset(k // self.units, k % self.units))
+                got = f.readinto(memoryview(buf))
+            assert got == self.unit_bytes, "short read of %s" % self.path
+            out[k] = lib.tsb_xxh64(buf.ctypes.data, buf.size, 0)
+
+        with ThreadPoolExecutor(threads or max(1, min(16, os.cpu_count() or 1))) as ex:
+            list(ex.map(one, range(n)))
+        tmp = side + ".%d.tmp" % os.getpid()
+        out.tofile(tmp)
+        os.replace(tmp, side)
+        self._hashes = [int(x) for x in out]
         return self._hashes
 
     def desc(self, tiers="pinned", order="ranked", engine="tsb-synth"):
