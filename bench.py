@@ -368,7 +368,7 @@ def main():
     # verify_hash with descriptor hashes: residents checked at the open, and every unit landed in a slot while decoding
     # hashed on the device against its descriptor hash (the landing check)
     run = harness.DgRun(model, resident_keys=resident_keys(1 + rank), spare_per_layer=a.spare, max_ids=TOP_K,
-                        diag=True, test_hooks=False, mode=1, slices=128, wb_defer=a.wb_defer, wb_stream=a.wb_stream,
+                        diag=True, test_hooks=False, mode=1, slices=512, wb_defer=a.wb_defer, wb_stream=a.wb_stream,
                         verify=hashed,
                         inclusive=inclusive, peer=setup.tier if setup else None,
                         disk_keys=disk_keys(a, resident_keys(1)) if a.file else (), disk_staging=a.staging,
@@ -435,14 +435,19 @@ def main():
         land_launches = j1["land_launches"] - j0["land_launches"]
         # (2) end to end: the same steps of a second trace window through the ABI with host buffers, the readers
         # computing the positional checksum (the reference GPU tests' check)
+        # one untimed step through the e2e path first (its graph's first launch, host buffers), on a token of its own
+        run.step(synth.zipf_trace(1, LAYERS, UNITS, TOP_K, s=ZIPF, seed=201 + rank)[0], mode=0)
         s2 = run.ctx.stats()
         outs2 = np.zeros((a.steps, LAYERS, TOP_K), dtype=np.uint64)
+        step_ms = []
         barrier()
         w0 = time.perf_counter()
         for t in range(a.steps):
+            ws = time.perf_counter()
             outs2[t] = run.step(ids2[t], mode=0)
             if a.round_every and (t + 1) % a.round_every == 0:
                 run.ctx.round()
+            step_ms.append((time.perf_counter() - ws) * 1e3)
         w1 = time.perf_counter()
         barrier()
         # every routed unit of both legs as its reader saw it, against the generator's sums
@@ -504,7 +509,9 @@ def main():
         "misses_per_token": round(misses / a.steps, 3), "lookups_per_token": round(lookups / a.steps, 3),
         "e2e": {"value": round(e2e, 3), "unit": "GB/s", "h2d_bytes_per_step": LAYERS * TOP_K * 4,
                 "d2h_bytes_per_step": LAYERS * TOP_K * 8,
-                "tokens_per_s": round(a.steps * world / e2e_s_max, 3)},
+                "tokens_per_s": round(a.steps * world / e2e_s_max, 3),
+                "step_ms": {"median": round(statistics.median(step_ms), 3), "min": round(min(step_ms), 3),
+                            "max": round(max(step_ms), 3)}},
         "roofline": {"bound": "link", "kernel": "miss service (demand copies + entries + ready on the demand stream)",
                      "achieved": round(achieved, 3) if achieved else None, "peak": round(peak, 3) if peak else None,
                      "unit": "GB/s", "frac": round(achieved / peak, 4) if achieved and peak else None, "traffic": None,

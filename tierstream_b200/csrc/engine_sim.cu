@@ -41,40 +41,51 @@ __device__ __forceinline__ uint64_t weighted16(const uint4& w, uint32_t m) {
   return v;
 }
 
-// grid (n, slices): block (i, s) reads slice s of unit ids[i] of gated layer g and adds its part of the checksum.
+// The checksum contribution of one 16-byte group at unit position 16 x e (m = that position % 251).
+__device__ __forceinline__ uint64_t group_sum(const uint4& w, uint32_t m, int mode) {
+  return mode == 1 ? uint64_t(w.x) + w.y + w.z + w.w : weighted16(w, m);
+}
+
+// grid (n, slices): block (i, s) reads slice s of unit ids[i] of gated layer g and adds its part of the checksum. A
+// slice is a range of the unit's 16-byte groups (its parts back to back); each part it covers is walked directly, four
+// 16-byte loads in flight per thread.
 __global__ __launch_bounds__(kThreads) void reader_kernel(ss_dg_device_view v, uint32_t g, const int32_t* ids,
                                                           uint32_t n, unsigned long long* out, int mode) {
   const uint32_t i = blockIdx.x;
   if (i >= n) return;
   const int32_t slot = ss_dg_slot(&v, g, ids[i]);
-  uint64_t unit_bytes = 0;
-  for (uint32_t p = 0; p < v.n_parts; ++p) unit_bytes += v.parts[p].bytes;
-  // slices of 16-byte vectors; every part is a multiple of 256 bytes in a gated layout
-  const uint64_t n16 = unit_bytes / 16;
+  uint64_t n16 = 0;
+  for (uint32_t p = 0; p < v.n_parts; ++p) n16 += v.parts[p].bytes / 16;  // every part is a multiple of 256 bytes
   const uint64_t per = (n16 + gridDim.y - 1) / gridDim.y;
   const uint64_t lo = per * blockIdx.y, hi = lo + per < n16 ? lo + per : n16;
-  uint64_t acc = 0;
-  // mode 0: the group at position pos weighs its byte k by (pos + k) % 251 + 1; m = pos % 251 steps by
-  // 16 x kThreads % 251 per iteration
-  constexpr uint32_t kStep = (16u * kThreads) % 251u;
-  uint32_t m = uint32_t(((lo + threadIdx.x) * 16) % 251);
-  for (uint64_t e = lo + threadIdx.x; e < hi; e += kThreads) {
-    const uint64_t pos = e * 16;  // position in the unit's bytes
-    uint32_t p = 0;
-    uint64_t off = pos;
-    while (p + 1 < v.n_parts && off >= v.parts[p].bytes) {
-      off -= v.parts[p].bytes;
-      ++p;
+  constexpr uint32_t kStep = (16u * kThreads) % 251u;  // m advances by this per kThreads groups
+  uint64_t acc = 0, first = 0;
+  for (uint32_t p = 0; p < v.n_parts; ++p) {
+    const uint64_t len = v.parts[p].bytes / 16;
+    const uint64_t a = lo > first ? lo : first, b = hi < first + len ? hi : first + len;
+    if (a < b) {
+      const uint4* base = reinterpret_cast<const uint4*>(static_cast<const char*>(v.parts[p].base) +
+                                                         uint64_t(slot) * v.parts[p].stride) - first;
+      uint64_t e = a + threadIdx.x;
+      uint32_t m = uint32_t((e * 16) % 251);
+      for (; e + 3 * kThreads < b; e += 4 * kThreads) {
+        uint4 w[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) w[k] = base[e + uint64_t(k) * kThreads];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          acc += group_sum(w[k], m, mode);
+          m += kStep;
+          if (m >= 251) m -= 251;
+        }
+      }
+      for (; e < b; e += kThreads) {
+        acc += group_sum(base[e], m, mode);
+        m += kStep;
+        if (m >= 251) m -= 251;
+      }
     }
-    const uint4 w = *reinterpret_cast<const uint4*>(static_cast<const char*>(v.parts[p].base) +
-                                                    uint64_t(slot) * v.parts[p].stride + off);
-    if (mode == 1) {
-      acc += uint64_t(w.x) + w.y + w.z + w.w;
-      continue;
-    }
-    acc += weighted16(w, m);
-    m += kStep;
-    if (m >= 251) m -= 251;
+    first += len;
   }
   __shared__ uint64_t part[kThreads / 32];
   acc = warp_sum(acc);
