@@ -64,7 +64,6 @@ def args_():
     p.add_argument("--wb-stream", type=int, default=1, help="ss_options.dg_wb_stream (the reference default 1)")
     p.add_argument("--spare", type=int, default=0,
                    help="spare slots per layer (dynamic_slots_per_layer); 0 = the workload's (1 Mixtral, 4 Qwen3)")
-    p.add_argument("--cpu-sample-tokens", type=int, default=6)
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--tier", default="auto", choices=["auto", "pinned", "peer", "file"],
                    help="where non-resident experts live: pinned RAM, or the peer tier (every expert owned by one "
@@ -259,6 +258,37 @@ def reference_sample(ids, tokens, a):
     return moved, dt
 
 
+def host_l3_bytes():
+    """The host's last-level cache per socket (bytes), from sysfs; None when not found."""
+    try:
+        with open("/sys/devices/system/cpu/cpu0/cache/index3/size") as f:
+            v = f.read().strip()
+        mult = {"K": 1 << 10, "M": 1 << 20, "G": 1 << 30}.get(v[-1:].upper(), 1)
+        return int(v.rstrip("KMGkmg")) * mult
+    except (OSError, ValueError):
+        return None
+
+
+def reference_measure(ids, a):
+    """The reference arm's measurement (also the in-line cpu_baseline): the reference DgCore with the memcpy transport
+    over warmup + steps tokens of the trace, less a run of the warm-up tokens alone (the replay cannot split them):
+    (GB/s, seconds of the timed tokens)."""
+    moved, dt = reference_sample(ids, a.warmup + a.steps, a)
+    w_moved, w_dt = reference_sample(ids, a.warmup, a) if a.warmup else (0, 0.0)
+    moved, dt = moved - w_moved, max(dt - w_dt, 1e-9)
+    return moved / dt / 1e9, dt
+
+
+def reference_sample_text(a, dt):
+    import oracle
+    l3 = host_l3_bytes()
+    return ("%d tokens of the trace (after %d warm-up tokens, subtracted) through the reference DgCore (oracle/_ref) "
+            "with a host memcpy transport on %d host threads, %.1f s; every copy moves its real bytes, slots and blocks "
+            "alias 16 unit buffers each (%.1f GB, host L3 %s)" % (
+                a.steps, a.warmup, int(oracle.ref().oref_copy_threads()), dt, 32 * 3 * PART / 1e9,
+                "%.0f MB" % (l3 / 1e6) if l3 else "unknown"))
+
+
 def run_reference(a):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
@@ -270,22 +300,14 @@ def run_reference(a):
         print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libtsref.so (the reference's sources "
                                                               "compiled by oracle/Makefile) is not built"}))
         return 0
-    moved, dt = reference_sample(ids, a.warmup + a.steps, a)
-    # the replay cannot split warm-up from timed tokens inside one call: time both and subtract the warm-up alone
-    w_moved, w_dt = reference_sample(ids, a.warmup, a) if a.warmup else (0, 0.0)
-    moved, dt = moved - w_moved, max(dt - w_dt, 1e-9)
-    v = moved / dt / 1e9
+    v, dt = reference_measure(ids, a)
     line = {"impl": "reference", "metric": METRIC, "value": round(v, 3), "unit": "GB/s", "n_gpus": a.gpus,
             "steps": a.steps, "warmup": a.warmup, "ms_per_step": round(dt * 1e3 / a.steps, 3),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u8", "data": "synthetic",
             "config": {"workload": WORKLOAD, "layers": LAYERS, "experts": UNITS, "part_bytes": PART,
                        "top_k": TOP_K, "zipf": ZIPF, "residents": RESIDENTS, "tokens": a.steps},
             "cpu_baseline": {"value": round(v, 3), "unit": "GB/s", "cores": int(oracle.ref().oref_copy_threads()),
-                             "kind": "reference",
-                             "sample": "%d tokens of the trace through the reference DgCore (oracle/_ref) with a "
-                                       "host memcpy transport on every host thread (every copy moves its bytes; slots "
-                                       "alias 4 buffers)"
-                                       % a.steps},
+                             "kind": "reference", "sample": reference_sample_text(a, dt)},
             "e2e": {"value": round(v, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line))
     return 0
@@ -474,6 +496,9 @@ def main():
             barrier()
             setup.close()
 
+    # the device-gated protocol's cost per layer when nothing misses (a small all-resident model, dg_overhead)
+    from tierstream_b200 import dg_overhead
+    zero_miss = dg_overhead.measure(layers=LAYERS, tokens=100, warmup=10)
     tot = torch.tensor([moved, moved_e2e, dev_ms, e2e_s, dma_ms], dtype=torch.float64, device="cuda")
     ver = torch.tensor([2 * a.steps, n1 + n0, bad1 + bad0], dtype=torch.int64, device="cuda")
     if dist:
@@ -530,6 +555,11 @@ def main():
                      "stores_checked": bool(a.peer and hashed)},
         "gpu_launches": int(a.steps * (2 + 2 * LAYERS) + land_launches + a.steps * LAYERS +
                             (c1["launches"] - c0["launches"])),
+        "dg_zero_miss_us_per_layer": zero_miss["overhead_us_per_layer"],
+        "dg_zero_miss": dict(zero_miss, how="rank 0: a %d-layer all-resident model (no token misses), the captured "
+                                            "token graph (begin, per layer export -> wait -> reader, end) less the "
+                                            "same readers captured alone, per layer; CUDA events, 100 tokens after 10 "
+                                            "warm-up" % LAYERS),
         "landing_check": dict(check, how="every unit copied into a slot hashed on the device (K3, xxh64) against "
                                           "its descriptor hash on a low-priority stream behind the layer's ready word; "
                                           "a copy into a slot still being hashed waits for it (hold_waits); each "
@@ -581,13 +611,12 @@ def main():
                            "pinned->HBM rate"})
         a.no_cpu_baseline = True  # the reference arm's sample is the pinned-RAM configuration
     if not a.no_cpu_baseline and world == 1:
-        smp = a.cpu_sample_tokens
-        mv, dt = reference_sample(synth.zipf_trace(smp, LAYERS, UNITS, TOP_K, s=ZIPF, seed=1), smp, a)
+        # the reference arm's own measurement (same trace, tokens and warm-up subtraction)
         import oracle
-        line["cpu_baseline"] = {"value": round(mv / dt / 1e9, 3), "unit": "GB/s",
+        v_ref, dt_ref = reference_measure(ids, a)
+        line["cpu_baseline"] = {"value": round(v_ref, 3), "unit": "GB/s",
                                 "cores": int(oracle.ref().oref_copy_threads()), "kind": "reference",
-                                "sample": "%d tokens through the reference DgCore with a host memcpy transport "
-                                          "on every host thread (oracle/_ref), %.1f s" % (smp, dt)}
+                                "sample": reference_sample_text(a, dt_ref)}
     print(json.dumps(line))
     if dist:
         dist.destroy_process_group()

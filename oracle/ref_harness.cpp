@@ -44,10 +44,11 @@ class HostTransport final : public ts::DgTransport {
   HostTransport(const oref_dg_config& c, uint32_t keys, uint32_t slots)
       : parts_(c.part_bytes, c.part_bytes + c.n_parts), table_(keys, -1), move_(c.move_bytes != 0) {
     for (uint64_t b : parts_) unit_ += b;
-    // move_bytes 2: a timing sample, every copy moves its real bytes but slots and blocks alias a ring of 4 unit
-    // buffers each (the bytes read back through the table are then not meaningful)
-    alias_slots_ = c.move_bytes == 2 ? 4 : slots;
-    alias_blocks_ = c.move_bytes == 2 ? 4 : c.blocks + c.disk_staging;
+    // move_bytes 2: a timing sample, every copy moves its real bytes but slots and blocks alias a ring of 16 unit
+    // buffers each, far above a host's last-level cache for the benchmark's units (the bytes read back through the
+    // table are then not meaningful)
+    alias_slots_ = c.move_bytes == 2 ? 16 : slots;
+    alias_blocks_ = c.move_bytes == 2 ? 16 : c.blocks + c.disk_staging;
     if (move_) {
       arena_.assign(size_t(alias_slots_) * unit_, 1);
       blocks_.assign(size_t(alias_blocks_) * unit_, 2);
