@@ -52,6 +52,13 @@ static void xfeed(xstate* s, const uint8_t* p, size_t len) {
   }
 }
 
+/* the final mix: xor-shifts by 33, 29 and 32 with multiplies by P2 and P3 between them */
+static uint64_t xavalanche(uint64_t h) {
+  h = (h ^ (h >> 33)) * P2;
+  h = (h ^ (h >> 29)) * P3;
+  return h ^ (h >> 32);
+}
+
 /* xxh64.cpp:77-106 (Xxh64::digest) */
 static uint64_t xdigest(const xstate* s) {
   uint64_t h;
@@ -62,32 +69,15 @@ static uint64_t xdigest(const xstate* s) {
     h = s->seed + P5;
   }
   h += s->total;
-  const uint8_t* p = s->buf;
-  size_t len = s->n;
-  while (len >= 8) {
-    h ^= xround(0, rd64(p));
-    h = rotl(h, 27) * P1 + P4;
-    p += 8;
-    len -= 8;
+  /* the buffered tail: 8-byte lanes, then one 4-byte word, then single bytes */
+  size_t at = 0;
+  for (; at + 8 <= s->n; at += 8) h = rotl(h ^ xround(0, rd64(s->buf + at)), 27) * P1 + P4;
+  if (at + 4 <= s->n) {
+    h = rotl(h ^ (uint64_t)rd32(s->buf + at) * P1, 23) * P2 + P3;
+    at += 4;
   }
-  if (len >= 4) {
-    h ^= (uint64_t)rd32(p) * P1;
-    h = rotl(h, 23) * P2 + P3;
-    p += 4;
-    len -= 4;
-  }
-  while (len) {
-    h ^= (uint64_t)(*p) * P5;
-    h = rotl(h, 11) * P1;
-    ++p;
-    --len;
-  }
-  h ^= h >> 33;
-  h *= P2;
-  h ^= h >> 29;
-  h *= P3;
-  h ^= h >> 32;
-  return h;
+  for (; at < s->n; ++at) h = rotl(h ^ (uint64_t)s->buf[at] * P5, 11) * P1;
+  return xavalanche(h);
 }
 
 uint64_t orc_xxh64(const void* data, size_t len, uint64_t seed) {

@@ -43,6 +43,23 @@ def test_ts_names_pair_with_ss_names():
             assert "ss_" + n[3:] in d
 
 
+def test_ts_names_are_aliases_of_ss_functions(lib):
+    """Every exported ts_* function is its ss_* function's own entry point (a linker alias), not a wrapper."""
+    import ctypes as C
+    addr = lambda n: C.cast(getattr(lib, n), C.c_void_p).value  # noqa: E731
+    ts_names = sorted(n for n in exported() if n.startswith("ts_"))
+    assert len(ts_names) > 150
+    for n in ts_names:
+        assert addr(n) == addr("ss_" + n[3:]), n
+
+
+def test_generated_ts_files_are_current():
+    """include/tierstream/ts.h and the alias script are what include/tierstream/gen_ts.py makes of ss.h."""
+    r = subprocess.run(["python", os.path.join(ROOT, "include", "tierstream", "gen_ts.py"), "--check"],
+                       capture_output=True, text=True)
+    assert r.returncode == 0, r.stdout + r.stderr
+
+
 def test_library_loads_and_reports(lib):
     assert lib.ss_abi_version() == 1
     assert lib.tsb_cuda_arch() == 100

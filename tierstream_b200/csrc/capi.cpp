@@ -36,36 +36,56 @@ namespace {
 
 thread_local std::string g_err;
 
+// Records `text` as this thread's last error and returns `st`.
+ss_status refuse(ss_status st, std::string text) {
+  g_err = std::move(text);
+  return st;
+}
+
+// Inside a catch block: the status the exception in flight maps to (a library error keeps its own; running out of
+// host memory is SS_E_NOMEM; anything else is an internal failure, SS_E_BACKEND), with its text kept as the last
+// error. `harmful` is set when a context that was running the call can no longer be trusted: every failure except a
+// library error other than SS_E_BACKEND / SS_E_NOMEM (bad arguments, IO, hash, capacity leave it consistent).
+ss_status caught(bool* harmful, const char* oom_text = "out of host memory") {
+  ss_status st = SS_E_BACKEND;
+  try {
+    throw;
+  } catch (const tsb::Error& e) {
+    g_err = e.what();
+    st = e.status();
+    *harmful = st == SS_E_BACKEND || st == SS_E_NOMEM;
+    return st;
+  } catch (const std::bad_alloc&) {
+    g_err = oom_text;
+    st = SS_E_NOMEM;
+  } catch (const std::exception& e) {
+    g_err = e.what();
+  } catch (...) {
+    g_err = "internal failure";
+  }
+  *harmful = true;
+  return st;
+}
+
+// A call outside any context: every exception becomes its status.
 template <class F>
 ss_status guard(F&& f) {
   try {
     f();
-    return SS_OK;
-  } catch (const tsb::Error& e) {
-    g_err = e.what();
-    return e.status();
-  } catch (const std::bad_alloc&) {
-    g_err = "out of host memory";
-    return SS_E_NOMEM;
-  } catch (const std::exception& e) {
-    g_err = e.what();
-    return SS_E_BACKEND;
+  } catch (...) {
+    bool harmful = false;
+    return caught(&harmful);
   }
+  return SS_OK;
 }
 
+// Hands `s` to the caller as a malloc'd, NUL-terminated copy (freed with ss_free), its length in *len.
 ss_status give_text(const std::string& s, char** out, size_t* len) {
-  if (!out) {
-    g_err = "null output pointer";
-    return SS_E_INVALID;
-  }
-  char* p = static_cast<char*>(std::malloc(s.size() + 1));
-  if (!p) {
-    g_err = "out of host memory";
-    return SS_E_NOMEM;
-  }
-  std::memcpy(p, s.data(), s.size());
-  p[s.size()] = 0;
-  *out = p;
+  if (!out) return refuse(SS_E_INVALID, "null output pointer");
+  char* copy = static_cast<char*>(std::malloc(s.size() + 1));
+  if (!copy) return refuse(SS_E_NOMEM, "out of host memory");
+  std::memcpy(copy, s.c_str(), s.size() + 1);  // with the terminator
+  *out = copy;
   if (len) *len = s.size();
   return SS_OK;
 }
@@ -167,34 +187,23 @@ tsb::DgContext& dg_of(const ss_ctx* c, const char* fn) {
   return *c->dg;
 }
 
-// Context calls: a poisoned context refuses; a device, allocation or internal failure poisons.
+// A context call: a poisoned context refuses it; a failure that leaves the context untrustworthy (`caught`) poisons
+// the context, so every later call is refused until it is closed. The calls run with the context's device current.
 template <class F>
 ss_status ctx_guard(ss_ctx* c, F&& f) {
-  if (!c) {
-    g_err = "null context";
-    return SS_E_INVALID;
-  }
-  if (ctx_poisoned(c)) {
-    g_err = "context poisoned by an earlier device, out-of-memory or internal failure: close it";
-    return SS_E_BACKEND;
-  }
+  if (!c) return refuse(SS_E_INVALID, "null context");
+  if (ctx_poisoned(c))
+    return refuse(SS_E_BACKEND, "context poisoned by an earlier device, out-of-memory or internal failure: close it");
   try {
     tsb::DeviceScope on(c->dg ? c->dg->device() : c->host->device());
     f();
-    return SS_OK;
-  } catch (const tsb::Error& e) {
-    if (e.status() == SS_E_BACKEND || e.status() == SS_E_NOMEM) ctx_poison(c);
-    g_err = e.what();
-    return e.status();
-  } catch (const std::bad_alloc&) {
-    ctx_poison(c);
-    g_err = "out of host memory (context poisoned)";
-    return SS_E_NOMEM;
-  } catch (const std::exception& e) {
-    ctx_poison(c);
-    g_err = e.what();
-    return SS_E_BACKEND;
+  } catch (...) {
+    bool harmful = false;
+    const ss_status st = caught(&harmful, "out of host memory (context poisoned)");
+    if (harmful) ctx_poison(c);
+    return st;
   }
+  return SS_OK;
 }
 
 }  // namespace
@@ -935,6 +944,19 @@ void round_defaults(ss_dg_round_params* p) {
   p->hysteresis = 1.25f;
   p->decay = 0.85f;
 }
+ss_dg_round_result round_result(const tsb::RoundOut& r) {
+  ss_dg_round_result x{};
+  x.promoted_to_device = r.promoted_to_device;
+  x.promoted_to_pinned = r.promoted_to_pinned;
+  x.demoted_from_device = r.demoted_from_device;
+  x.dropped_to_file = r.dropped_to_file;
+  x.cancelled = r.cancelled;
+  x.bytes_read = r.bytes_read;
+  x.bytes_h2d = r.bytes_h2d;
+  x.bytes_written_back = r.bytes_written_back;
+  x.ns = r.ns;
+  return x;
+}
 }  // namespace
 void ss_dg_round_defaults_sized(ss_dg_round_params* p, uint32_t size) { sized_defaults(p, size, round_defaults); }
 ss_status ss_dg_round_sized(ss_ctx* c, const ss_dg_round_params* p, ss_dg_round_result* out, uint32_t size) {
@@ -948,35 +970,21 @@ ss_status ss_dg_round_sized(ss_ctx* c, const ss_dg_round_params* p, ss_dg_round_
     in.hysteresis = double(v.hysteresis);
     in.decay = double(v.decay);
     tsb::DgContext& dg = dg_of(c, "ss_dg_round");
-    auto fill = [&] {  // on success, and on a failure after the round began
-      if (!out) return;
-      const tsb::RoundOut& r = dg.last_round();
-      ss_dg_round_result x{};
-      x.promoted_to_device = r.promoted_to_device;
-      x.promoted_to_pinned = r.promoted_to_pinned;
-      x.demoted_from_device = r.demoted_from_device;
-      x.dropped_to_file = r.dropped_to_file;
-      x.cancelled = r.cancelled;
-      x.bytes_read = r.bytes_read;
-      x.bytes_h2d = r.bytes_h2d;
-      x.bytes_written_back = r.bytes_written_back;
-      x.ns = r.ns;
-      give_sized(out, size, x);
-    };
-    try {
-      dg.round(in);
-    } catch (...) {
-      fill();
-      throw;
-    }
-    fill();
+    // the result is written however the round ends: a failure after the round began still reports the moves it made
+    struct ReportOnExit {
+      const tsb::DgContext& dg;
+      ss_dg_round_result* out;
+      uint32_t size;
+      ~ReportOnExit() {
+        if (out) give_sized(out, size, round_result(dg.last_round()));
+      }
+    } report{dg, out, size};
+    dg.round(in);
   });
 }
+// Any thread: one atomic store, no context state read (a poisoned or busy context is the engine's to report).
 ss_status ss_dg_round_cancel(ss_ctx* c) {
-  if (!c || !c->dg) {
-    g_err = "ss_dg_round_cancel: not a device-gated context";
-    return SS_E_INVALID;
-  }
+  if (!c || !c->dg) return refuse(SS_E_INVALID, "ss_dg_round_cancel: not a device-gated context");
   c->dg->round_cancel();
   return SS_OK;
 }

@@ -1,7 +1,13 @@
+// The strix-stream/desc-v1 descriptor (desc.hpp): reading, checking and writing it. The format (keys, defaults,
+// accepted values, limits, the rules a descriptor must satisfy) is the reference's (desc.cpp:126-441 there), so the
+// same manifests load and write back the same document. Here every JSON object is read through a Scope that knows
+// its path for messages and which keys it allows; each record type has a reader and a writer of its own.
 #include "desc.hpp"
 
+#include <algorithm>
 #include <cstdio>
-#include <set>
+#include <functional>
+#include <unordered_set>
 
 #include "errors.hpp"
 
@@ -9,269 +15,359 @@ namespace tsb {
 namespace {
 
 const char* const kSchema = "strix-stream/desc-v1";
-constexpr int kMaxLayers = 4096;
-constexpr int kMaxUnits = 1 << 16;
+const char* const kSchemaRenamed = "tierstream/desc-v1";  // the same schema under the project's later name
+constexpr uint64_t kLayerLimit = 4096, kUnitLimit = 1 << 16, kSourceLimit = 1024;
+constexpr uint64_t kTotalLimit = uint64_t(1) << 56;
 
-uint64_t capped(uint64_t v, uint64_t max, const std::string& where) {
-  require(v <= max, SS_E_DESC, where + ": " + std::to_string(v) + " is above the limit " + std::to_string(max));
-  return v;
-}
-uint64_t add_ck(uint64_t a, uint64_t b, const std::string& where) {
-  require(a <= UINT64_MAX - b, SS_E_DESC, where + ": byte arithmetic overflows 64 bits");
+// One JSON object being read: its path (for messages) and its keys.
+class Scope {
+ public:
+  Scope(const Json& j, std::string path) : j_(j), path_(std::move(path)) {}
+  const std::string& path() const { return path_; }
+  std::string at(const char* key) const { return path_ + "." + key; }
+  // Keys outside `known` are refused, except adapter notes ("x-" prefixed).
+  void known(std::initializer_list<const char*> keys) const {
+    require(j_.is_object(), SS_E_DESC, path_ + ": expected an object");
+    for (const auto& [k, v] : j_.obj) {
+      (void)v;
+      const bool note = k.compare(0, 2, "x-") == 0;
+      require(note || std::any_of(keys.begin(), keys.end(), [&](const char* x) { return k == x; }), SS_E_DESC,
+              path_ + ": unknown key \"" + k + "\"");
+    }
+  }
+  const Json* opt(const char* key) const { return j_.find(key); }
+  const Json& req(const char* key) const {
+    const Json* v = j_.find(key);
+    require(v != nullptr, SS_E_DESC, path_ + ": missing \"" + key + "\"");
+    return *v;
+  }
+  uint64_t u64(const char* key) const { return json_u64(req(key), at(key)); }
+  uint64_t u64(const char* key, uint64_t dflt) const {
+    const Json* v = opt(key);
+    return v ? json_u64(*v, at(key)) : dflt;
+  }
+  // An optional count with an upper limit.
+  uint64_t count(const char* key, uint64_t dflt, uint64_t limit) const {
+    const uint64_t v = u64(key, dflt);
+    require(v <= limit, SS_E_DESC, at(key) + ": " + std::to_string(v) + " is above the limit " + std::to_string(limit));
+    return v;
+  }
+  std::string str(const char* key) const { return json_str(req(key), at(key)); }
+  std::string str(const char* key, const std::string& dflt) const {
+    const Json* v = opt(key);
+    return v ? json_str(*v, at(key)) : dflt;
+  }
+  // An optional array: f(element, its path) per element.
+  void each(const char* key, const std::function<void(const Json&, const std::string&)>& f) const {
+    const Json* v = opt(key);
+    if (!v) return;
+    require(v->is_array(), SS_E_DESC, at(key) + ": expected an array");
+    for (size_t i = 0; i < v->arr.size(); ++i) f(v->arr[i], at(key) + "[" + std::to_string(i) + "]");
+  }
+
+ private:
+  const Json& j_;
+  std::string path_;
+};
+
+// Byte arithmetic of the checks: an overflow refuses the descriptor.
+uint64_t sum_or_refuse(uint64_t a, uint64_t b, const std::string& where) {
+  require(b <= UINT64_MAX - a, SS_E_DESC, where + ": byte arithmetic overflows 64 bits");
   return a + b;
 }
-uint64_t mul_ck(uint64_t a, uint64_t b, const std::string& where) {
+uint64_t product_or_refuse(uint64_t a, uint64_t b, const std::string& where) {
   require(a == 0 || b <= UINT64_MAX / a, SS_E_DESC, where + ": byte arithmetic overflows 64 bits");
   return a * b;
 }
-std::string idx(const std::string& base, size_t i) { return base + "[" + std::to_string(i) + "]"; }
 
-const Json& need(const Json& o, const char* key, const std::string& where) {
-  const Json* v = o.find(key);
-  require(v != nullptr, SS_E_DESC, where + ": missing \"" + key + "\"");
-  return *v;
+bool is_pow2(uint64_t v) { return v && !(v & (v - 1)); }
+
+// Tensor formats a part may name (and any "x-" adapter format).
+bool format_known(const std::string& f) {
+  static const std::unordered_set<std::string> names = {
+      "F32",   "F16",   "BF16",  "FP8_E4M3", "FP8_E5M2", "EXL3",    "MXFP4",  "NVFP4",  "Q2_K",
+      "Q3_K",  "Q4_K",  "Q5_K",  "Q6_K",     "Q8_0",     "Q4_0",    "Q4_1",   "Q5_0",   "Q5_1",
+      "IQ1_S", "IQ1_M", "IQ2_XXS", "IQ2_XS", "IQ2_S",    "IQ3_XXS", "IQ3_S",  "IQ4_NL", "IQ4_XS",
+      "TQ1_0", "TQ2_0", "I8",    "U8",    "mixed"};
+  return names.count(f) > 0 || f.compare(0, 2, "x-") == 0;
 }
-uint64_t u64_or(const Json& o, const char* key, const std::string& where, uint64_t dflt) {
-  const Json* v = o.find(key);
-  return v ? json_u64(*v, where + "." + key) : dflt;
-}
-std::string str_or(const Json& o, const char* key, const std::string& where, const std::string& dflt = "") {
-  const Json* v = o.find(key);
-  return v ? json_str(*v, where + "." + key) : dflt;
-}
-// Unknown keys are errors, except "x-" adapter notes.
-void only_keys(const Json& o, const std::string& where, std::initializer_list<const char*> allowed) {
-  require(o.is_object(), SS_E_DESC, where + ": expected an object");
-  std::set<std::string> ok(allowed.begin(), allowed.end());
-  for (const auto& kv : o.obj)
-    require(kv.first.rfind("x-", 0) == 0 || ok.count(kv.first), SS_E_DESC,
-            where + ": unknown key \"" + kv.first + "\"");
-}
-std::vector<NamedBytes> named(const Json* v, const std::string& where) {
-  std::vector<NamedBytes> out;
-  if (!v) return out;
-  require(v->is_array(), SS_E_DESC, where + ": expected an array");
-  for (size_t i = 0; i < v->arr.size(); ++i) {
-    const std::string w = idx(where, i);
-    only_keys(v->arr[i], w, {"name", "bytes"});
-    out.push_back({json_str(need(v->arr[i], "name", w), w + ".name"), json_u64(need(v->arr[i], "bytes", w), w + ".bytes")});
-  }
-  return out;
-}
-bool known_format(const std::string& f) {
-  static const std::set<std::string> k = {"F32",    "F16",   "BF16",    "FP8_E4M3", "FP8_E5M2", "EXL3",   "MXFP4",
-                                          "NVFP4",  "Q2_K",  "Q3_K",    "Q4_K",     "Q5_K",     "Q6_K",   "Q8_0",
-                                          "Q4_0",   "Q4_1",  "Q5_0",    "Q5_1",     "IQ1_S",    "IQ1_M",  "IQ2_XXS",
-                                          "IQ2_XS", "IQ2_S", "IQ3_XXS", "IQ3_S",    "IQ4_NL",   "IQ4_XS", "TQ1_0",
-                                          "TQ2_0",  "I8",    "U8",      "mixed"};
-  return k.count(f) || f.rfind("x-", 0) == 0;
-}
-std::string hex16(uint64_t v) {
-  char b[17];
-  std::snprintf(b, sizeof b, "%016llx", (unsigned long long)v);
-  return b;
-}
-uint64_t from_hex16(const std::string& s, const std::string& where) {
+
+// xxh64 values are 16 lowercase hex digits.
+uint64_t parse_xxh(const std::string& s, const std::string& where) {
   require(s.size() == 16, SS_E_DESC, where + ": expected 16 hex digits");
   uint64_t v = 0;
   for (char c : s) {
-    v <<= 4;
-    if (c >= '0' && c <= '9') v |= uint64_t(c - '0');
-    else if (c >= 'a' && c <= 'f') v |= uint64_t(c - 'a' + 10);
-    else fail(SS_E_DESC, where + ": expected lowercase hex digits");
+    int nib = -1;
+    if (c >= '0' && c <= '9') nib = c - '0';
+    else if (c >= 'a' && c <= 'f') nib = 10 + (c - 'a');
+    require(nib >= 0, SS_E_DESC, where + ": expected lowercase hex digits");
+    v = v << 4 | uint64_t(nib);
   }
   return v;
 }
-// "strix-stream/desc-v1" and the renamed "tierstream/desc-v1" are the same schema.
-bool schema_ok(const std::string& s) { return s == kSchema || s == "tierstream/desc-v1"; }
+std::string print_xxh(uint64_t v) {
+  char buf[17];
+  std::snprintf(buf, sizeof buf, "%016llx", static_cast<unsigned long long>(v));
+  return buf;
+}
+
+const char* kind_name(LayerKind k) {
+  return k == LayerKind::Dense ? "dense" : k == LayerKind::Moe ? "moe" : "blob";
+}
+
+// ---- readers ----
+std::vector<NamedBytes> read_named(const Scope& s, const char* key) {
+  std::vector<NamedBytes> out;
+  s.each(key, [&](const Json& e, const std::string& path) {
+    const Scope r(e, path);
+    r.known({"name", "bytes"});
+    out.push_back(NamedBytes{r.str("name"), r.u64("bytes")});
+  });
+  return out;
+}
+
+Part read_part(const Scope& r) {
+  r.known({"name", "format", "source", "offset", "stride", "bytes"});
+  Part p;
+  p.name = r.str("name", "");
+  p.format = r.str("format");
+  p.source = int(r.count("source", 0, kSourceLimit));
+  p.offset = r.u64("offset");
+  p.bytes = r.u64("bytes");
+  p.stride = r.u64("stride", p.bytes);
+  return p;
+}
+
+Router read_router(const Scope& r) {
+  r.known({"tensor", "bias", "format", "score", "rows", "cols"});
+  Router x;
+  x.tensor = r.str("tensor");
+  x.bias = r.str("bias", "");
+  x.format = r.str("format", "F32");
+  x.score = r.str("score", "softmax");
+  x.rows = uint32_t(r.count("rows", 0, kUnitLimit));
+  x.cols = uint32_t(r.count("cols", 0, uint64_t(1) << 24));
+  return x;
+}
+
+Layer read_layer(const Scope& r) {
+  r.known({"index", "kind", "fixed_bytes", "n_units", "top_k", "n_shared", "unit_bytes", "parts", "router", "hash",
+           "benefit", "streamable"});
+  Layer l;
+  const int64_t index = json_i64(r.req("index"), r.at("index"));
+  require(index >= 0 && uint64_t(index) < kLayerLimit, SS_E_DESC, r.at("index") + ": 0..4095");
+  l.index = int(index);
+  const std::string kind = r.str("kind");
+  if (kind == "dense") l.kind = LayerKind::Dense;
+  else if (kind == "moe") l.kind = LayerKind::Moe;
+  else if (kind == "blob") l.kind = LayerKind::Blob;
+  else fail(SS_E_DESC, r.at("kind") + ": expected dense | moe | blob");
+  l.fixed_bytes = r.u64("fixed_bytes", 0);
+  l.n_units = int(r.count("n_units", l.kind == LayerKind::Blob ? 1 : 0, kUnitLimit));
+  l.top_k = int(r.count("top_k", 0, kUnitLimit));
+  l.n_shared = int(r.count("n_shared", 0, kUnitLimit));
+  l.unit_bytes = r.u64("unit_bytes", 0);
+  if (const Json* v = r.opt("streamable")) l.streamable = json_bool(*v, r.at("streamable"));
+  r.each("parts", [&](const Json& e, const std::string& path) { l.parts.push_back(read_part(Scope(e, path))); });
+  if (const Json* v = r.opt("router")) {
+    l.router = read_router(Scope(*v, r.at("router")));
+    l.has_router = true;
+  }
+  if (const Json* v = r.opt("hash"))
+    require(v->is_array(), SS_E_DESC, r.at("hash") + ": expected an array of xxh64 hex strings");
+  r.each("hash", [&](const Json& e, const std::string& path) { l.hash.push_back(parse_xxh(json_str(e, path), path)); });
+  r.each("benefit", [&](const Json& e, const std::string& path) { l.benefit.push_back(json_f64(e, path)); });
+  return l;
+}
+
+LookupTable read_table(const Scope& r) {
+  r.known({"name", "source", "offset", "rows", "row_bytes", "placement"});
+  LookupTable t;
+  t.name = r.str("name");
+  t.source = int(r.count("source", 0, kSourceLimit));
+  t.offset = r.u64("offset", 0);
+  t.rows = r.u64("rows");
+  t.row_bytes = r.u64("row_bytes");
+  t.placement = r.str("placement", "file");
+  return t;
+}
+
+// ---- the rules a layer with units must satisfy; fills its unit bytes when omitted ----
+void check_units(Layer& l, const std::string& path, const Desc& d) {
+  require(!l.parts.empty(), SS_E_DESC, path + ".parts: a layer with units needs parts");
+  uint64_t total = 0;
+  for (size_t i = 0; i < l.parts.size(); ++i) {
+    const Part& p = l.parts[i];
+    const std::string pp = path + ".parts[" + std::to_string(i) + "]";
+    require(p.bytes > 0, SS_E_DESC, pp + ".bytes: > 0");
+    require(format_known(p.format), SS_E_DESC, pp + ".format: unknown format " + p.format);
+    require(p.source >= 0 && size_t(p.source) < d.sources.size(), SS_E_DESC, pp + ".source: no such source");
+    require(l.n_units == 1 || p.stride >= p.bytes, SS_E_DESC, pp + ".stride: >= bytes (units overlap)");
+    total = sum_or_refuse(total, p.bytes, pp);
+    // the last unit's piece ends inside 64-bit offsets
+    const uint64_t last = sum_or_refuse(p.offset, product_or_refuse(uint64_t(l.n_units - 1), p.stride, pp), pp);
+    (void)sum_or_refuse(last, p.bytes, pp);
+  }
+  if (!l.unit_bytes) l.unit_bytes = total;
+  require(l.unit_bytes == total, SS_E_DESC,
+          path + ".unit_bytes: " + std::to_string(l.unit_bytes) + " != sum of parts " + std::to_string(total));
+  (void)product_or_refuse(sum_or_refuse(l.unit_bytes, d.unit_align, path), uint64_t(l.n_units), path);
+  require(l.hash.empty() || l.hash.size() == size_t(l.n_units), SS_E_DESC, path + ".hash: one per unit");
+  require(l.benefit.empty() || l.benefit.size() == size_t(l.n_units), SS_E_DESC, path + ".benefit: one per unit");
+  require(!l.has_router || l.router.rows == 0 || l.router.rows == uint32_t(l.n_units), SS_E_DESC,
+          path + ".router.rows: must equal n_units");
+}
+
+// ---- writers ----
+Json named_json(const std::vector<NamedBytes>& v) {
+  Json a = Json::array();
+  for (const NamedBytes& n : v) {
+    Json o = Json::object();
+    o["name"] = Json::string(n.name);
+    o["bytes"] = Json::number(n.bytes);
+    a.push(o);
+  }
+  return a;
+}
+
+Json part_json(const Part& p) {
+  Json o = Json::object();
+  if (!p.name.empty()) o["name"] = Json::string(p.name);
+  o["format"] = Json::string(p.format);
+  o["source"] = Json::number(int64_t(p.source));
+  for (const auto& [k, v] : {std::pair<const char*, uint64_t>{"offset", p.offset}, {"stride", p.stride},
+                             {"bytes", p.bytes}})
+    o[k] = Json::number(v);
+  return o;
+}
+
+Json layer_json(const Layer& l) {
+  Json o = Json::object();
+  o["index"] = Json::number(int64_t(l.index));
+  o["kind"] = Json::string(kind_name(l.kind));
+  o["fixed_bytes"] = Json::number(l.fixed_bytes);
+  if (l.n_units > 0) {  // a layer without units carries no unit fields
+    o["n_units"] = Json::number(int64_t(l.n_units));
+    o["unit_bytes"] = Json::number(l.unit_bytes);
+    o["streamable"] = Json::boolean(l.streamable);
+    Json parts = Json::array();
+    for (const Part& p : l.parts) parts.push(part_json(p));
+    o["parts"] = parts;
+    if (!l.hash.empty()) {
+      Json h = Json::array();
+      for (uint64_t v : l.hash) h.push(Json::string(print_xxh(v)));
+      o["hash"] = h;
+    }
+    if (!l.benefit.empty()) {
+      Json b = Json::array();
+      for (double v : l.benefit) b.push(Json::number(v));
+      o["benefit"] = b;
+    }
+  }
+  if (l.top_k) o["top_k"] = Json::number(int64_t(l.top_k));
+  if (l.n_shared) o["n_shared"] = Json::number(int64_t(l.n_shared));
+  if (l.has_router) {
+    Json r = Json::object();
+    const Router& x = l.router;
+    for (const auto& [k, v] : {std::pair<const char*, const std::string*>{"tensor", &x.tensor}, {"bias", &x.bias},
+                               {"format", &x.format}, {"score", &x.score}})
+      if (k != std::string("bias") || !v->empty()) r[k] = Json::string(*v);  // an empty bias is left out
+    r["rows"] = Json::number(uint64_t(x.rows));
+    r["cols"] = Json::number(uint64_t(x.cols));
+    o["router"] = r;
+  }
+  return o;
+}
 
 }  // namespace
 
 const char* tiers_name(Tiers t) {
-  switch (t) {
-    case Tiers::Pinned: return "pinned";
-    case Tiers::Disk: return "disk";
-    case Tiers::PinnedDisk: return "pinned|disk";
-    case Tiers::Pair: return "pair";
-  }
-  return "?";
+  static const char* const names[] = {"pinned", "disk", "pinned|disk", "pair"};  // in Tiers order
+  const size_t i = size_t(t);
+  return i < sizeof names / sizeof names[0] ? names[i] : "?";
 }
 const char* order_name(Order o) { return o == Order::Prefix ? "prefix" : "ranked"; }
 
 uint64_t Desc::fixed_total() const {
   uint64_t t = 0;
-  for (const auto& n : fixed_device) t += n.bytes;
-  for (size_t L = 0; L < layers.size(); ++L) {
-    t += layers[L].fixed_bytes;
-    if (!layers[L].streamable) t += uint64_t(layers[L].n_units) * unit_stride(int(L));
-  }
+  for (const NamedBytes& n : fixed_device) t += n.bytes;
+  for (size_t L = 0; L < layers.size(); ++L)
+    t += layers[L].fixed_bytes + (layers[L].streamable ? 0 : uint64_t(layers[L].n_units) * unit_stride(int(L)));
   return t;
 }
 
 Desc desc_from_json(const Json& j) {
-  const std::string w = "desc";
-  only_keys(j, w, {"schema", "model", "engine", "fixed_device", "host_fixed", "state_bytes_per_position",
-                   "workspace_bytes_per_row", "unit_align", "sources", "order", "tiers", "ring_slots", "routes",
-                   "layers", "lookup_tables"});
-  require(schema_ok(json_str(need(j, "schema", w), "desc.schema")), SS_E_DESC,
+  const Scope top(j, "desc");
+  top.known({"schema", "model", "engine", "fixed_device", "host_fixed", "state_bytes_per_position",
+             "workspace_bytes_per_row", "unit_align", "sources", "order", "tiers", "ring_slots", "routes", "layers",
+             "lookup_tables"});
+  const std::string schema = top.str("schema");
+  require(schema == kSchema || schema == kSchemaRenamed, SS_E_DESC,
           std::string("desc.schema: expected \"") + kSchema + "\"");
   Desc d;
-  d.model = str_or(j, "model", w);
-  d.engine = str_or(j, "engine", w);
-  d.fixed_device = named(j.find("fixed_device"), "desc.fixed_device");
-  d.host_fixed = named(j.find("host_fixed"), "desc.host_fixed");
-  d.state_bytes_per_position = u64_or(j, "state_bytes_per_position", w, 0);
-  d.workspace_bytes_per_row = u64_or(j, "workspace_bytes_per_row", w, 0);
-  d.unit_align = u64_or(j, "unit_align", w, 256);
-  d.ring_slots = uint32_t(capped(u64_or(j, "ring_slots", w, 0), 1u << 20, "desc.ring_slots"));
-  d.routes = str_or(j, "routes", w);
-  const std::string order = str_or(j, "order", w, "ranked");
-  if (order == "prefix") d.order = Order::Prefix;
-  else if (order == "ranked") d.order = Order::Ranked;
-  else fail(SS_E_DESC, "desc.order: expected prefix | ranked");
-  const std::string tiers = str_or(j, "tiers", w, "pinned|disk");
-  if (tiers == "pinned") d.tiers = Tiers::Pinned;
-  else if (tiers == "disk") d.tiers = Tiers::Disk;
-  else if (tiers == "pinned|disk") d.tiers = Tiers::PinnedDisk;
-  else if (tiers == "pair") d.tiers = Tiers::Pair;
-  else fail(SS_E_DESC, "desc.tiers: expected pinned | disk | pinned|disk | pair");
-  if (const Json* s = j.find("sources")) {
-    require(s->is_array(), SS_E_DESC, "desc.sources: expected an array");
-    for (size_t i = 0; i < s->arr.size(); ++i) {
-      const std::string sw = idx("desc.sources", i);
-      only_keys(s->arr[i], sw, {"name", "path", "align"});
-      Source src;
-      src.name = str_or(s->arr[i], "name", sw);
-      src.path = json_str(need(s->arr[i], "path", sw), sw + ".path");
-      src.align = u64_or(s->arr[i], "align", sw, 4096);
-      d.sources.push_back(src);
+  d.model = top.str("model", "");
+  d.engine = top.str("engine", "");
+  d.fixed_device = read_named(top, "fixed_device");
+  d.host_fixed = read_named(top, "host_fixed");
+  d.state_bytes_per_position = top.u64("state_bytes_per_position", 0);
+  d.workspace_bytes_per_row = top.u64("workspace_bytes_per_row", 0);
+  d.unit_align = top.u64("unit_align", 256);
+  d.ring_slots = uint32_t(top.count("ring_slots", 0, uint64_t(1) << 20));
+  d.routes = top.str("routes", "");
+  const std::string order = top.str("order", "ranked");
+  require(order == "prefix" || order == "ranked", SS_E_DESC, "desc.order: expected prefix | ranked");
+  d.order = order == "prefix" ? Order::Prefix : Order::Ranked;
+  const std::string tiers = top.str("tiers", "pinned|disk");
+  bool tiers_ok = false;
+  for (Tiers t : {Tiers::Pinned, Tiers::Disk, Tiers::PinnedDisk, Tiers::Pair})
+    if (tiers == tiers_name(t)) {
+      d.tiers = t;
+      tiers_ok = true;
     }
-  }
-  const Json& layers = need(j, "layers", w);
+  require(tiers_ok, SS_E_DESC, "desc.tiers: expected pinned | disk | pinned|disk | pair");
+  top.each("sources", [&](const Json& e, const std::string& path) {
+    const Scope r(e, path);
+    r.known({"name", "path", "align"});
+    d.sources.push_back(Source{r.str("name", ""), r.str("path"), r.u64("align", 4096)});
+  });
+  const Json& layers = top.req("layers");
   require(layers.is_array(), SS_E_DESC, "desc.layers: expected an array");
-  for (size_t i = 0; i < layers.arr.size(); ++i) {
-    const Json& lj = layers.arr[i];
-    const std::string lw = idx("desc.layers", i);
-    only_keys(lj, lw, {"index", "kind", "fixed_bytes", "n_units", "top_k", "n_shared", "unit_bytes", "parts",
-                       "router", "hash", "benefit", "streamable"});
-    Layer l;
-    const int64_t index = json_i64(need(lj, "index", lw), lw + ".index");
-    require(index >= 0 && index < kMaxLayers, SS_E_DESC, lw + ".index: 0..4095");
-    l.index = int(index);
-    const std::string kind = json_str(need(lj, "kind", lw), lw + ".kind");
-    if (kind == "dense") l.kind = LayerKind::Dense;
-    else if (kind == "moe") l.kind = LayerKind::Moe;
-    else if (kind == "blob") l.kind = LayerKind::Blob;
-    else fail(SS_E_DESC, lw + ".kind: expected dense | moe | blob");
-    l.fixed_bytes = u64_or(lj, "fixed_bytes", lw, 0);
-    l.n_units = int(capped(u64_or(lj, "n_units", lw, l.kind == LayerKind::Blob ? 1 : 0), kMaxUnits, lw + ".n_units"));
-    l.top_k = int(capped(u64_or(lj, "top_k", lw, 0), kMaxUnits, lw + ".top_k"));
-    l.n_shared = int(capped(u64_or(lj, "n_shared", lw, 0), kMaxUnits, lw + ".n_shared"));
-    l.unit_bytes = u64_or(lj, "unit_bytes", lw, 0);
-    if (const Json* st = lj.find("streamable")) l.streamable = json_bool(*st, lw + ".streamable");
-    if (const Json* parts = lj.find("parts")) {
-      require(parts->is_array(), SS_E_DESC, lw + ".parts: expected an array");
-      for (size_t p = 0; p < parts->arr.size(); ++p) {
-        const Json& pj = parts->arr[p];
-        const std::string pw = idx(lw + ".parts", p);
-        only_keys(pj, pw, {"name", "format", "source", "offset", "stride", "bytes"});
-        Part part;
-        part.name = str_or(pj, "name", pw);
-        part.format = json_str(need(pj, "format", pw), pw + ".format");
-        part.source = int(capped(u64_or(pj, "source", pw, 0), 1024, pw + ".source"));
-        part.offset = json_u64(need(pj, "offset", pw), pw + ".offset");
-        part.bytes = json_u64(need(pj, "bytes", pw), pw + ".bytes");
-        part.stride = u64_or(pj, "stride", pw, part.bytes);
-        l.parts.push_back(part);
-      }
-    }
-    if (const Json* r = lj.find("router")) {
-      const std::string rw = lw + ".router";
-      only_keys(*r, rw, {"tensor", "bias", "format", "score", "rows", "cols"});
-      l.has_router = true;
-      l.router.tensor = json_str(need(*r, "tensor", rw), rw + ".tensor");
-      l.router.bias = str_or(*r, "bias", rw);
-      l.router.format = str_or(*r, "format", rw, "F32");
-      l.router.score = str_or(*r, "score", rw, "softmax");
-      l.router.rows = uint32_t(capped(u64_or(*r, "rows", rw, 0), kMaxUnits, rw + ".rows"));
-      l.router.cols = uint32_t(capped(u64_or(*r, "cols", rw, 0), 1u << 24, rw + ".cols"));
-    }
-    if (const Json* h = lj.find("hash")) {
-      require(h->is_array(), SS_E_DESC, lw + ".hash: expected an array of xxh64 hex strings");
-      for (size_t k = 0; k < h->arr.size(); ++k)
-        l.hash.push_back(from_hex16(json_str(h->arr[k], idx(lw + ".hash", k)), idx(lw + ".hash", k)));
-    }
-    if (const Json* b = lj.find("benefit")) {
-      require(b->is_array(), SS_E_DESC, lw + ".benefit: expected an array");
-      for (size_t k = 0; k < b->arr.size(); ++k) l.benefit.push_back(json_f64(b->arr[k], idx(lw + ".benefit", k)));
-    }
-    d.layers.push_back(std::move(l));
-  }
-  if (const Json* t = j.find("lookup_tables")) {
-    require(t->is_array(), SS_E_DESC, "desc.lookup_tables: expected an array");
-    for (size_t i = 0; i < t->arr.size(); ++i) {
-      const std::string tw = idx("desc.lookup_tables", i);
-      only_keys(t->arr[i], tw, {"name", "source", "offset", "rows", "row_bytes", "placement"});
-      LookupTable lt;
-      lt.name = json_str(need(t->arr[i], "name", tw), tw + ".name");
-      lt.source = int(capped(u64_or(t->arr[i], "source", tw, 0), 1024, tw + ".source"));
-      lt.offset = u64_or(t->arr[i], "offset", tw, 0);
-      lt.rows = json_u64(need(t->arr[i], "rows", tw), tw + ".rows");
-      lt.row_bytes = json_u64(need(t->arr[i], "row_bytes", tw), tw + ".row_bytes");
-      lt.placement = str_or(t->arr[i], "placement", tw, "file");
-      d.lookup_tables.push_back(lt);
-    }
-  }
+  top.each("layers", [&](const Json& e, const std::string& path) { d.layers.push_back(read_layer(Scope(e, path))); });
+  top.each("lookup_tables", [&](const Json& e, const std::string& path) {
+    d.lookup_tables.push_back(read_table(Scope(e, path)));
+  });
   desc_validate(d);
   return d;
 }
 
 void desc_validate(Desc& d) {
-  require(!d.layers.empty() && d.layers.size() <= size_t(kMaxLayers), SS_E_DESC, "desc.layers: 1..4096 layers");
-  require(d.unit_align >= 1 && (d.unit_align & (d.unit_align - 1)) == 0, SS_E_DESC, "desc.unit_align: power of two");
-  for (size_t s = 0; s < d.sources.size(); ++s) {
-    const uint64_t a = d.sources[s].align;
-    require(a >= 1 && (a & (a - 1)) == 0 && a <= (1u << 20), SS_E_DESC,
-            idx("desc.sources", s) + ".align: power of two <= 1 MiB");
-  }
+  require(!d.layers.empty() && d.layers.size() <= kLayerLimit, SS_E_DESC, "desc.layers: 1..4096 layers");
+  require(is_pow2(d.unit_align), SS_E_DESC, "desc.unit_align: power of two");
+  for (size_t s = 0; s < d.sources.size(); ++s)
+    require(is_pow2(d.sources[s].align) && d.sources[s].align <= (uint64_t(1) << 20), SS_E_DESC,
+            "desc.sources[" + std::to_string(s) + "].align: power of two <= 1 MiB");
   d.unit_base.assign(d.layers.size(), 0);
   d.total_units = 0;
   d.max_unit_bytes = 0;
   d.max_units_per_layer = 0;
   for (size_t i = 0; i < d.layers.size(); ++i) {
     Layer& l = d.layers[i];
-    const std::string lw = idx("desc.layers", i);
-    require(l.index == int(i), SS_E_DESC, lw + ".index: layers must be listed in order 0..n-1");
-    if (l.kind == LayerKind::Dense)
-      require(l.n_units == 0 && l.parts.empty(), SS_E_DESC, lw + ": a dense layer has no units (use fixed_bytes)");
-    else if (l.kind == LayerKind::Blob)
-      require(l.n_units == 1, SS_E_DESC, lw + ": a blob layer has exactly one unit");
-    else {
-      require(l.n_units >= 1, SS_E_DESC, lw + ": a moe layer needs n_units >= 1");
-      require(l.top_k >= 1 && l.top_k <= l.n_units, SS_E_DESC, lw + ".top_k: 1..n_units");
+    const std::string path = "desc.layers[" + std::to_string(i) + "]";
+    require(l.index == int(i), SS_E_DESC, path + ".index: layers must be listed in order 0..n-1");
+    switch (l.kind) {
+      case LayerKind::Dense:
+        require(l.n_units == 0 && l.parts.empty(), SS_E_DESC, path + ": a dense layer has no units (use fixed_bytes)");
+        break;
+      case LayerKind::Blob:
+        require(l.n_units == 1, SS_E_DESC, path + ": a blob layer has exactly one unit");
+        break;
+      case LayerKind::Moe:
+        require(l.n_units >= 1, SS_E_DESC, path + ": a moe layer needs n_units >= 1");
+        require(l.top_k >= 1 && l.top_k <= l.n_units, SS_E_DESC, path + ".top_k: 1..n_units");
+        break;
     }
     if (l.n_units > 0) {
-      require(!l.parts.empty(), SS_E_DESC, lw + ".parts: a layer with units needs parts");
-      uint64_t sum = 0;
-      for (size_t p = 0; p < l.parts.size(); ++p) {
-        const Part& part = l.parts[p];
-        const std::string pw = idx(lw + ".parts", p);
-        require(part.bytes > 0, SS_E_DESC, pw + ".bytes: > 0");
-        require(known_format(part.format), SS_E_DESC, pw + ".format: unknown format " + part.format);
-        require(part.source >= 0 && size_t(part.source) < d.sources.size(), SS_E_DESC, pw + ".source: no such source");
-        require(l.n_units == 1 || part.stride >= part.bytes, SS_E_DESC, pw + ".stride: >= bytes (units overlap)");
-        sum = add_ck(sum, part.bytes, pw);
-        add_ck(add_ck(part.offset, mul_ck(uint64_t(l.n_units - 1), part.stride, pw), pw), part.bytes, pw);
-      }
-      if (l.unit_bytes == 0) l.unit_bytes = sum;
-      require(l.unit_bytes == sum, SS_E_DESC,
-              lw + ".unit_bytes: " + std::to_string(l.unit_bytes) + " != sum of parts " + std::to_string(sum));
-      mul_ck(add_ck(l.unit_bytes, d.unit_align, lw), uint64_t(l.n_units), lw);
-      require(l.hash.empty() || l.hash.size() == size_t(l.n_units), SS_E_DESC, lw + ".hash: one per unit");
-      require(l.benefit.empty() || l.benefit.size() == size_t(l.n_units), SS_E_DESC, lw + ".benefit: one per unit");
-      if (l.has_router)
-        require(l.router.rows == 0 || l.router.rows == uint32_t(l.n_units), SS_E_DESC,
-                lw + ".router.rows: must equal n_units");
+      check_units(l, path, d);
       if (l.streamable) {
         d.max_unit_bytes = std::max(d.max_unit_bytes, l.unit_bytes);
         d.max_units_per_layer = std::max(d.max_units_per_layer, l.n_units);
@@ -280,121 +376,71 @@ void desc_validate(Desc& d) {
     d.unit_base[i] = d.total_units;
     d.total_units += l.n_units;
   }
-  uint64_t dev = 0, host = 0;
-  for (const auto& n : d.fixed_device) dev = add_ck(dev, n.bytes, "desc.fixed_device");
-  for (const auto& n : d.host_fixed) host = add_ck(host, n.bytes, "desc.host_fixed");
-  uint64_t all = add_ck(dev, host, "desc");
-  for (size_t L = 0; L < d.layers.size(); ++L)
-    all = add_ck(all, mul_ck(uint64_t(d.layers[L].n_units), add_ck(d.layers[L].unit_bytes, 4096, idx("desc.layers", L)),
-                             idx("desc.layers", L)),
-                 idx("desc.layers", L));
-  require(all < (uint64_t(1) << 56), SS_E_DESC, "desc: total bytes above 2^56 (64 PiB)");
+  // every byte the model names (with a page of slack per unit) stays below 64 PiB
+  uint64_t device = 0, host = 0;
+  for (const NamedBytes& n : d.fixed_device) device = sum_or_refuse(device, n.bytes, "desc.fixed_device");
+  for (const NamedBytes& n : d.host_fixed) host = sum_or_refuse(host, n.bytes, "desc.host_fixed");
+  uint64_t everything = sum_or_refuse(device, host, "desc");
   for (size_t L = 0; L < d.layers.size(); ++L) {
-    dev = add_ck(dev, d.layers[L].fixed_bytes, idx("desc.layers", L) + ".fixed_bytes");
+    const std::string path = "desc.layers[" + std::to_string(L) + "]";
+    const uint64_t per = sum_or_refuse(d.layers[L].unit_bytes, 4096, path);
+    everything = sum_or_refuse(everything, product_or_refuse(uint64_t(d.layers[L].n_units), per, path), path);
+  }
+  require(everything < kTotalLimit, SS_E_DESC, "desc: total bytes above 2^56 (64 PiB)");
+  // the device's fixed bytes, non-streamable units included, stay within 64 bits
+  for (size_t L = 0; L < d.layers.size(); ++L) {
+    const std::string path = "desc.layers[" + std::to_string(L) + "]";
+    device = sum_or_refuse(device, d.layers[L].fixed_bytes, path + ".fixed_bytes");
     if (!d.layers[L].streamable)
-      dev = add_ck(dev, mul_ck(uint64_t(d.layers[L].n_units), d.unit_stride(int(L)), idx("desc.layers", L)),
-                   idx("desc.layers", L));
+      device = sum_or_refuse(device, product_or_refuse(uint64_t(d.layers[L].n_units), d.unit_stride(int(L)), path),
+                             path);
   }
   for (size_t i = 0; i < d.lookup_tables.size(); ++i) {
     const LookupTable& t = d.lookup_tables[i];
-    const std::string tw = idx("desc.lookup_tables", i);
-    require(t.source >= 0 && size_t(t.source) < d.sources.size(), SS_E_DESC, tw + ".source: no such source");
+    const std::string path = "desc.lookup_tables[" + std::to_string(i) + "]";
+    require(t.source >= 0 && size_t(t.source) < d.sources.size(), SS_E_DESC, path + ".source: no such source");
     require(t.placement == "file" || t.placement == "pinned" || t.placement == "device", SS_E_DESC,
-            tw + ".placement: file | pinned | device");
+            path + ".placement: file | pinned | device");
   }
 }
 
 Json desc_to_json(const Desc& d) {
   Json j = Json::object();
   j["schema"] = Json::string(kSchema);
-  if (!d.model.empty()) j["model"] = Json::string(d.model);
-  if (!d.engine.empty()) j["engine"] = Json::string(d.engine);
-  auto list = [](const std::vector<NamedBytes>& v) {
-    Json a = Json::array();
-    for (const auto& n : v) {
-      Json e = Json::object();
-      e["name"] = Json::string(n.name);
-      e["bytes"] = Json::number(n.bytes);
-      a.push(e);
-    }
-    return a;
-  };
-  j["fixed_device"] = list(d.fixed_device);
-  j["host_fixed"] = list(d.host_fixed);
-  j["state_bytes_per_position"] = Json::number(d.state_bytes_per_position);
-  j["workspace_bytes_per_row"] = Json::number(d.workspace_bytes_per_row);
-  j["unit_align"] = Json::number(d.unit_align);
+  for (const auto& [k, v] : {std::pair<const char*, const std::string*>{"model", &d.model}, {"engine", &d.engine},
+                             {"routes", &d.routes}})
+    if (!v->empty()) j[k] = Json::string(*v);
+  j["fixed_device"] = named_json(d.fixed_device);
+  j["host_fixed"] = named_json(d.host_fixed);
+  for (const auto& [k, v] : {std::pair<const char*, uint64_t>{"state_bytes_per_position", d.state_bytes_per_position},
+                             {"workspace_bytes_per_row", d.workspace_bytes_per_row},
+                             {"unit_align", d.unit_align},
+                             {"ring_slots", d.ring_slots}})
+    j[k] = Json::number(v);
   j["order"] = Json::string(order_name(d.order));
   j["tiers"] = Json::string(tiers_name(d.tiers));
-  j["ring_slots"] = Json::number(uint64_t(d.ring_slots));
-  if (!d.routes.empty()) j["routes"] = Json::string(d.routes);
-  Json srcs = Json::array();
-  for (const auto& s : d.sources) {
-    Json e = Json::object();
-    if (!s.name.empty()) e["name"] = Json::string(s.name);
-    e["path"] = Json::string(s.path);
-    e["align"] = Json::number(s.align);
-    srcs.push(e);
+  Json sources = Json::array();
+  for (const Source& s : d.sources) {
+    Json o = Json::object();
+    if (!s.name.empty()) o["name"] = Json::string(s.name);
+    o["path"] = Json::string(s.path);
+    o["align"] = Json::number(s.align);
+    sources.push(o);
   }
-  j["sources"] = srcs;
+  j["sources"] = sources;
   Json layers = Json::array();
-  for (const auto& l : d.layers) {
-    Json e = Json::object();
-    e["index"] = Json::number(int64_t(l.index));
-    e["kind"] = Json::string(l.kind == LayerKind::Dense ? "dense" : l.kind == LayerKind::Moe ? "moe" : "blob");
-    e["fixed_bytes"] = Json::number(l.fixed_bytes);
-    if (l.n_units > 0) {
-      e["n_units"] = Json::number(int64_t(l.n_units));
-      e["unit_bytes"] = Json::number(l.unit_bytes);
-      e["streamable"] = Json::boolean(l.streamable);
-      Json parts = Json::array();
-      for (const auto& p : l.parts) {
-        Json pj = Json::object();
-        if (!p.name.empty()) pj["name"] = Json::string(p.name);
-        pj["format"] = Json::string(p.format);
-        pj["source"] = Json::number(int64_t(p.source));
-        pj["offset"] = Json::number(p.offset);
-        pj["stride"] = Json::number(p.stride);
-        pj["bytes"] = Json::number(p.bytes);
-        parts.push(pj);
-      }
-      e["parts"] = parts;
-      if (!l.hash.empty()) {
-        Json h = Json::array();
-        for (uint64_t v : l.hash) h.push(Json::string(hex16(v)));
-        e["hash"] = h;
-      }
-      if (!l.benefit.empty()) {
-        Json b = Json::array();
-        for (double v : l.benefit) b.push(Json::number(v));
-        e["benefit"] = b;
-      }
-    }
-    if (l.top_k) e["top_k"] = Json::number(int64_t(l.top_k));
-    if (l.n_shared) e["n_shared"] = Json::number(int64_t(l.n_shared));
-    if (l.has_router) {
-      Json r = Json::object();
-      r["tensor"] = Json::string(l.router.tensor);
-      if (!l.router.bias.empty()) r["bias"] = Json::string(l.router.bias);
-      r["format"] = Json::string(l.router.format);
-      r["score"] = Json::string(l.router.score);
-      r["rows"] = Json::number(uint64_t(l.router.rows));
-      r["cols"] = Json::number(uint64_t(l.router.cols));
-      e["router"] = r;
-    }
-    layers.push(e);
-  }
+  for (const Layer& l : d.layers) layers.push(layer_json(l));
   j["layers"] = layers;
   Json tables = Json::array();
-  for (const auto& t : d.lookup_tables) {
-    Json e = Json::object();
-    e["name"] = Json::string(t.name);
-    e["source"] = Json::number(int64_t(t.source));
-    e["offset"] = Json::number(t.offset);
-    e["rows"] = Json::number(t.rows);
-    e["row_bytes"] = Json::number(t.row_bytes);
-    e["placement"] = Json::string(t.placement);
-    tables.push(e);
+  for (const LookupTable& t : d.lookup_tables) {
+    Json o = Json::object();
+    o["name"] = Json::string(t.name);
+    o["source"] = Json::number(int64_t(t.source));
+    o["offset"] = Json::number(t.offset);
+    o["rows"] = Json::number(t.rows);
+    o["row_bytes"] = Json::number(t.row_bytes);
+    o["placement"] = Json::string(t.placement);
+    tables.push(o);
   }
   j["lookup_tables"] = tables;
   return j;

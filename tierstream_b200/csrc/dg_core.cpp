@@ -1,15 +1,27 @@
+// The device-gated slot cache (dg_core.hpp states its rules). The state: one Entry per gated key (its home, slot,
+// block and flags), the recency list and the pinned homes' list (KeyList: links kept per list), the free slots and
+// free blocks (LifoPool), the write-backs in flight (wbs_) and deferred (deferred_), the file reads in flight
+// (pending_), and the scored eviction's per-layer history (sc_).
 #include "dg_core.hpp"
 
 #include <algorithm>
 #include <chrono>
 #include <cmath>
+#include <numeric>
 
 #include "errors.hpp"
 
 namespace tsb {
 
+namespace {
+using Clock = std::chrono::steady_clock;
+uint64_t ns_since(Clock::time_point t0) {
+  return uint64_t(std::chrono::duration_cast<std::chrono::nanoseconds>(Clock::now() - t0).count());
+}
+}  // namespace
+
 SlotCache::SlotCache(const CacheConfig& cfg, Mover* m) : c_(cfg), m_(m) {
-  base_.assign(1, 0);
+  base_ = {0};
   for (uint32_t n : c_.n_units) {
     require(n >= 1, SS_E_INVALID, "device-gated: a gated layer without units");
     base_.push_back(base_.back() + n);
@@ -17,24 +29,24 @@ SlotCache::SlotCache(const CacheConfig& cfg, Mover* m) : c_(cfg), m_(m) {
   keys_ = base_.back();
   require(c_.persistent_slots >= 1 && c_.spare_target <= c_.persistent_slots, SS_E_INVALID,
           "device-gated: spare target above the persistent slots");
-  const uint64_t slots = uint64_t(c_.persistent_slots) + 2ull * c_.bank_slots;
-  require(slots < 0x7fffffffull, SS_E_INVALID, "device-gated: more than 2^31 - 1 slots");
-  slots_ = uint32_t(slots);
+  const uint64_t all_slots = uint64_t(c_.persistent_slots) + 2ull * c_.bank_slots;
+  require(all_slots < 0x7fffffffull, SS_E_INVALID, "device-gated: more than 2^31 - 1 slots");
+  slots_ = uint32_t(all_slots);
   bank_first_ = c_.persistent_slots;
-  require(c_.inclusive == 0 || c_.inclusive < c_.blocks, SS_E_INVALID,
+  require(!c_.inclusive || c_.inclusive < c_.blocks, SS_E_INVALID,
           "device-gated: the inclusive share must leave a block for write-backs");
   require(!c_.disk_tier || c_.disk_staging >= 1, SS_E_INVALID, "device-gated: the file tier needs staging buffers");
   require(c_.disk_tier || (!c_.disk_prefetch && !c_.disk_staging && !c_.home_blocks), SS_E_INVALID,
           "device-gated: file tier options without the file tier");
   require(uint64_t(c_.blocks) + c_.disk_staging < 0x7fffffffull, SS_E_INVALID, "device-gated: too many host blocks");
-  stage_ev_.assign(c_.disk_staging, nullptr);
   require(!c_.no_admit || c_.bank_slots >= c_.max_ids, SS_E_CAPACITY,
           "device-gated: dg_no_admit serves every miss through a bank slot: it needs " + std::to_string(c_.max_ids) +
               " bank slots per bank (dg_max_ids), " + std::to_string(c_.bank_slots) + " configured");
+  stage_ev_.assign(c_.disk_staging, nullptr);
   run_.assign(c_.n_units.size(), 1);
   rs_.assign(keys_, 0.0);
   rhits_.assign(keys_, 0);
-  if (c_.scored) {  // every score table allocated now (the service thread never allocates)
+  if (c_.scored) {  // the history's tables exist from the open (the service thread never allocates)
     require(c_.w_trans <= 1000 && c_.w_freq <= 1000 && c_.w_rec <= 1000 && c_.w_trans + c_.w_freq + c_.w_rec == 1000,
             SS_E_INVALID, "device-gated: score weights must each be 0..1000 and sum to 1000");
     require(c_.max_ids >= 1 && c_.max_ids <= 64, SS_E_INVALID, "device-gated: score unions need max ids 1..64");
@@ -44,19 +56,21 @@ SlotCache::SlotCache(const CacheConfig& cfg, Mover* m) : c_(cfg), m_(m) {
       require(n <= 65536, SS_E_INVALID,
               "device-gated: scored eviction needs at most 65536 units per gated layer (gated layer " +
                   std::to_string(g) + " has " + std::to_string(n) + ")");
-      LayerScore& l = sc_[g];
-      l.T.assign(n * n, 0);
-      l.rowsum.assign(n, 0);
-      l.cnt.assign(n, 0);
-      l.ring.assign(size_t(kWindow) * c_.max_ids, 0);
-      l.ring_len.assign(kWindow, 0);
-      l.prev.reserve(c_.max_ids);
-      l.cur.reserve(c_.max_ids);
+      LayerScore& h = sc_[g];
+      h.T.assign(n * n, 0);
+      h.rowsum.assign(n, 0);
+      h.cnt.assign(n, 0);
+      h.ring.assign(size_t(kWindow) * c_.max_ids, 0);
+      h.ring_len.assign(kWindow, 0);
+      h.prev.reserve(c_.max_ids);
+      h.cur.reserve(c_.max_ids);
     }
     select_heap_.reserve(c_.persistent_slots);
   }
   e_.assign(keys_, Entry{});
   table_.assign(keys_, -1);
+  recent_.reset(keys_);
+  homes_.reset(keys_);
   bank_key_.assign(2u * size_t(c_.bank_slots), kNil);
   pf_layer_.assign(gated(), 0);
   layer_missed_.assign(gated(), 0);
@@ -69,7 +83,7 @@ SlotCache::SlotCache(const CacheConfig& cfg, Mover* m) : c_(cfg), m_(m) {
 }
 
 SlotCache::~SlotCache() {
-  for (const Pending& p : pending_) {  // reads in flight end before anything they write into can be freed
+  for (const Pending& p : pending_) {  // a read in flight ends before the buffer it writes can be freed
     try {
       m_->read_end(p.handle);
     } catch (...) {
@@ -91,194 +105,205 @@ uint32_t SlotCache::gated_of(uint32_t k) const {
 }
 
 uint32_t SlotCache::coming() const {
-  uint32_t n = 0;
-  for (uint32_t k : coming_) n += e_[k].home == Home::Coming ? 1u : 0u;
-  return n;
+  return uint32_t(std::count_if(coming_.begin(), coming_.end(), [&](uint32_t k) { return e_[k].home == Home::Coming; }));
 }
 
 void SlotCache::apply_wb_defer() {
-  if (c_.wb_defer) {
-    wb_stream_ = c_.wb_on_d2h ? Mover::kD2h : Mover::kDem;
-    layer_bytes_ = c_.wb_layer_bytes ? c_.wb_layer_bytes : m_->part_bytes(0);
-    max_outstanding_ = c_.wb_max_outstanding ? c_.wb_max_outstanding : 2 * unit_bytes_;
-    require(layer_bytes_ <= uint64_t(INT64_MAX) / 4, SS_E_INVALID, "device-gated: dg_wb_layer_bytes too large");
-    if (c_.wb_on_d2h && !post_ready_ev_) post_ready_ev_ = event();
-  } else {
-    wb_stream_ = Mover::kDem;
-    layer_bytes_ = 0;
-    max_outstanding_ = 0;
+  layer_bytes_ = max_outstanding_ = 0;
+  wb_stream_ = Mover::kDem;
+  if (!c_.wb_defer) return;
+  if (c_.wb_on_d2h) wb_stream_ = Mover::kD2h;
+  layer_bytes_ = c_.wb_layer_bytes ? c_.wb_layer_bytes : m_->part_bytes(0);
+  max_outstanding_ = c_.wb_max_outstanding ? c_.wb_max_outstanding : 2 * unit_bytes_;
+  require(layer_bytes_ <= uint64_t(INT64_MAX) / 4, SS_E_INVALID, "device-gated: dg_wb_layer_bytes too large");
+  if (c_.wb_on_d2h && !post_ready_ev_) post_ready_ev_ = event();
+}
+
+// ---- small steps shared by the decisions ----
+void SlotCache::touch(uint32_t k) {
+  if (recent_.has(k)) recent_.erase(k);
+  recent_.push_front(k);
+  if (c_.scored) {  // unique stamps, larger nearer the front (stamp_room keeps the counter far from wrapping)
+    if (stamp_ == UINT64_MAX) broken("the recency stamp counter wrapped");
+    e_[k].lru_stamp = ++stamp_;
   }
 }
 
-void SlotCache::place(const std::vector<uint32_t>& order, const std::vector<uint8_t>* disk) {
-  drain_pending();
-  const uint32_t dev_max = c_.persistent_slots - c_.spare_target;
-  std::vector<uint8_t> taken(keys_, 0);
-  std::vector<uint32_t> dev;
-  for (uint32_t k : order) {
-    require(k < keys_, SS_E_INVALID, "device-gated: resident key out of range");
-    if (!taken[k] && dev.size() < dev_max) {
-      taken[k] = 1;
-      dev.push_back(k);
-    }
-  }
-  // file tier: which non-resident keys get a block, as flags (the plan's pinned units first, then its disk units,
-  // each by priority: the order's keys first, then key order); host_rank is their recency order
-  const bool three = c_.disk_tier;
-  std::vector<uint8_t> blocked(keys_, 0);
-  std::vector<uint32_t> host_rank;
-  if (three) {
-    require(!disk || disk->size() == keys_, SS_E_INVALID, "device-gated: the disk flags do not cover the keys");
-    std::vector<uint8_t> seen(keys_, 0);
-    std::vector<uint32_t> prio;
-    for (uint32_t k : order)
-      if (!seen[k]) {
-        seen[k] = 1;
-        prio.push_back(k);
-      }
-    for (uint32_t k = 0; k < keys_; ++k)
-      if (!seen[k]) prio.push_back(k);
-    const uint32_t cap = std::min(c_.home_blocks, c_.blocks);
-    for (uint8_t pass = 0; pass < 2; ++pass)
-      for (uint32_t k : prio)
-        if (!taken[k] && (disk ? (*disk)[k] : uint8_t(0)) == pass && host_rank.size() < cap) {
-          blocked[k] = 1;
-          host_rank.push_back(k);
-        }
-  } else {
-    require(uint64_t(keys_) - dev.size() <= c_.blocks, SS_E_CAPACITY,
-            "device-gated: fewer host blocks than non-resident units");
-  }
-  int32_t next_block = 0;
-  on_file_ = 0;
-  hhead_ = htail_ = kNil;
-  for (uint32_t k = 0; k < keys_; ++k) {
-    e_[k] = Entry{};
-    if (!taken[k] && (!three || blocked[k])) {
-      e_[k].block = next_block++;  // Host home, blocks in key order
-    } else if (!taken[k]) {
-      e_[k].home = Home::File;
-      ++on_file_;
-    }
-    table_[k] = -1;
-  }
-  for (size_t i = host_rank.size(); i-- > 0;) hpush(host_rank[i]);  // the first by priority most recently homed
-  head_ = tail_ = kNil;
-  for (uint32_t i = 0; i < dev.size(); ++i) {
-    Entry& x = e_[dev[i]];
-    x.home = Home::Device;
-    x.slot = int32_t(i);
-    table_[dev[i]] = x.slot;
-  }
-  for (size_t i = dev.size(); i-- > 0;) push_front(dev[i]);  // dev[0] ends up most recent
-  on_device_ = uint32_t(dev.size());
-  free_slots_.clear();
-  free_blocks_.clear();
-  for (uint32_t s = c_.persistent_slots; s-- > on_device_;) free_slots_.push_back(int32_t(s));
-  for (int32_t b = int32_t(c_.blocks); b-- > next_block;) free_blocks_.push_back(b);
-  open_c_ = c_;
-  open_e_ = e_;
-  open_table_ = table_;
-  open_free_slots_ = free_slots_;
-  open_free_blocks_ = free_blocks_;
-  open_head_ = head_;
-  open_tail_ = tail_;
-  open_on_device_ = on_device_;
-  open_hhead_ = hhead_;
-  open_htail_ = htail_;
-  open_on_file_ = on_file_;
-  open_stamp_ = stamp_;
+void SlotCache::leave_device(uint32_t k) {
+  if (recent_.has(k)) recent_.erase(k);
+  --on_device_;
+  table_[k] = -1;
 }
 
-// ---- file tier: the pinned homes' recency list (head = most recently homed; only kept with the file tier) ----
-void SlotCache::hpush(uint32_t k) {
+void SlotCache::home_push(uint32_t k, bool cold) {
   if (!c_.disk_tier) return;
-  Entry& x = e_[k];
-  x.hprev = kNil;
-  x.hnext = hhead_;
-  if (hhead_ != kNil) e_[hhead_].hprev = k;
-  else htail_ = k;
-  hhead_ = k;
-  x.in_hlist = true;
+  if (cold) homes_.push_back(k);  // the least recently homed: the first to drop to its file
+  else homes_.push_front(k);
 }
 
-void SlotCache::hunlink(uint32_t k) {
+void SlotCache::home_erase(uint32_t k) {
   if (!c_.disk_tier) return;
-  Entry& x = e_[k];
-  if (!x.in_hlist) broken("a pinned home outside the pinned recency list");
-  if (x.hprev != kNil) e_[x.hprev].hnext = x.hnext;
-  else hhead_ = x.hnext;
-  if (x.hnext != kNil) e_[x.hnext].hprev = x.hprev;
-  else htail_ = x.hprev;
-  x.hprev = x.hnext = kNil;
-  x.in_hlist = false;
+  if (!homes_.has(k)) broken("a pinned home outside the pinned recency list");
+  homes_.erase(k);
 }
 
-void SlotCache::hpush_tail(uint32_t k) {  // the least recently homed: the first to drop to its file
-  if (!c_.disk_tier) return;
-  Entry& x = e_[k];
-  x.hnext = kNil;
-  x.hprev = htail_;
-  if (htail_ != kNil) e_[htail_].hnext = k;
-  else hhead_ = k;
-  htail_ = k;
-  x.in_hlist = true;
+void SlotCache::recycle(void*& ev) {
+  if (!ev) return;
+  pool_.push_back(ev);
+  ev = nullptr;
+}
+
+void SlotCache::count_fetch(uint32_t g, bool prefetch, int delta) {
+  uint64_t& total = prefetch ? st_.prefetched : st_.fetched;
+  uint64_t& layer = prefetch ? lc_[g].prefetched : lc_[g].fetched;
+  total += uint64_t(int64_t(delta));
+  layer += uint64_t(int64_t(delta));
+}
+
+void SlotCache::count_evicted(uint32_t k) { bump(gated_of(k), &CacheStats::evicted, &LayerCounts::evicted); }
+
+void SlotCache::stamp_room(const char* what) const {
+  if (c_.scored && stamp_ > kStampLimit)
+    fail(SS_E_BACKEND, std::string("device-gated: ") + what +
+                           ": the scored eviction's recency stamp counter is exhausted (reopen the context)");
+}
+
+void* SlotCache::event() {
+  if (pool_.empty()) {
+    all_events_.push_back(m_->event_create());
+    return all_events_.back();
+  }
+  void* ev = pool_.back();
+  pool_.pop_back();
+  return ev;
+}
+
+void SlotCache::publish(Mover::Stream s, uint32_t k, int32_t v) {
+  table_[k] = v;
+  m_->publish(s, k, v);
 }
 
 std::vector<uint32_t> SlotCache::host_order() const {
   std::vector<uint32_t> out;
-  for (uint32_t k = hhead_; k != kNil; k = e_[k].hnext) out.push_back(k);
+  for (uint32_t k = homes_.front(); k != kNil; k = homes_.older(k)) out.push_back(k);
   return out;
 }
 
+// ---- the open placement ----
+void SlotCache::place(const std::vector<uint32_t>& order, const std::vector<uint8_t>* disk) {
+  drain_pending();
+  // residents: the first distinct keys of `order`, as many as leave the spare target free
+  const uint32_t room = c_.persistent_slots - c_.spare_target;
+  std::vector<uint8_t> resident(keys_, 0);
+  std::vector<uint32_t> dev;
+  for (uint32_t k : order) {
+    require(k < keys_, SS_E_INVALID, "device-gated: resident key out of range");
+    if (resident[k] || dev.size() >= room) continue;
+    resident[k] = 1;
+    dev.push_back(k);
+  }
+  // pinned homes: every other key, or with the file tier min(home_blocks, blocks) of them (the plan's pinned units
+  // before its disk units, each group by priority: `order` first, then key order); `ranked` is their recency order
+  std::vector<uint8_t> gets_block(keys_, 0);
+  std::vector<uint32_t> ranked;
+  if (c_.disk_tier) {
+    require(!disk || disk->size() == keys_, SS_E_INVALID, "device-gated: the disk flags do not cover the keys");
+    std::vector<uint32_t> by_priority;
+    std::vector<uint8_t> listed(keys_, 0);
+    auto list = [&](uint32_t k) {
+      if (!listed[k]) by_priority.push_back(k);
+      listed[k] = 1;
+    };
+    for (uint32_t k : order) list(k);
+    for (uint32_t k = 0; k < keys_; ++k) list(k);
+    const size_t cap = std::min(c_.home_blocks, c_.blocks);
+    for (uint8_t want_disk : {uint8_t(0), uint8_t(1)})
+      for (uint32_t k : by_priority) {
+        const uint8_t is_disk = disk ? (*disk)[k] : uint8_t(0);
+        if (ranked.size() >= cap) break;
+        if (resident[k] || is_disk != want_disk) continue;
+        gets_block[k] = 1;
+        ranked.push_back(k);
+      }
+  } else {
+    require(uint64_t(keys_) - dev.size() <= c_.blocks, SS_E_CAPACITY,
+            "device-gated: fewer host blocks than non-resident units");
+  }
+  int32_t blocks_used = 0;
+  on_file_ = 0;
+  homes_.reset(keys_);
+  recent_.reset(keys_);
+  for (uint32_t k = 0; k < keys_; ++k) {
+    Entry& x = e_[k] = Entry{};
+    table_[k] = -1;
+    if (resident[k]) continue;
+    if (c_.disk_tier && !gets_block[k]) {
+      x.home = Home::File;
+      ++on_file_;
+    } else {
+      x.block = blocks_used++;  // a pinned home; blocks in key order
+    }
+  }
+  for (auto it = ranked.rbegin(); it != ranked.rend(); ++it) home_push(*it);  // ranked[0] most recently homed
+  for (uint32_t i = 0; i < dev.size(); ++i) {
+    e_[dev[i]].home = Home::Device;
+    e_[dev[i]].slot = int32_t(i);
+    table_[dev[i]] = int32_t(i);
+  }
+  for (auto it = dev.rbegin(); it != dev.rend(); ++it) touch(*it);  // dev[0] most recent
+  on_device_ = uint32_t(dev.size());
+  free_slots_.fill_down(int32_t(c_.persistent_slots), int32_t(on_device_));
+  free_blocks_.fill_down(int32_t(c_.blocks), blocks_used);
+  open_ = OpenState{c_, e_, table_, free_slots_, free_blocks_, recent_, homes_, on_device_, on_file_, stamp_};
+}
+
+// ---- file tier ----
 // A unit that leaves the device or a bank slot without a write-back: its block (a clean copy, or the block it was
 // served from) is its home again, else (file tier) its file.
 void SlotCache::to_lower(uint32_t k, bool cold) {
   Entry& x = e_[k];
   x.slot = -1;
-  if (x.backed) {
-    x.backed = false;
-    --backed_;
-  }
-  if (x.block >= 0) {
-    x.home = Home::Host;
-    if (cold) hpush_tail(k);
-    else hpush(k);
-  } else {
+  if (x.backed) --backed_;
+  x.backed = false;
+  if (x.block < 0) {
     if (!c_.disk_tier) broken("a unit without a block left the device without a write-back");
     x.home = Home::File;
     ++on_file_;
+    return;
   }
+  x.home = Home::Host;
+  home_push(k, cold);
 }
 
 // The least recently homed pinned unit (not skipped) goes to its file (no copy: the file holds its bytes); its block
 // is free.
 bool SlotCache::drop_host_lru(const std::vector<uint8_t>* skip, bool count) {
   if (!c_.disk_tier) return false;
-  uint32_t k = htail_;
-  while (k != kNil && skip && (*skip)[k]) k = e_[k].hprev;
+  uint32_t k = homes_.back();
+  for (; k != kNil && skip && (*skip)[k]; k = homes_.newer(k)) {
+  }
   if (k == kNil) return false;
   Entry& x = e_[k];
-  hunlink(k);
-  free_blocks_.push_back(x.block);
+  home_erase(k);
+  free_blocks_.give(x.block);
   x.block = -1;
   x.home = Home::File;
   ++on_file_;
-  if (count) ++st_.disk_drops;
+  st_.disk_drops += count ? 1 : 0;
   return true;
 }
 
 // The next staging buffer in rotation, once a read still holding it ended and its last copy landed.
 int32_t SlotCache::take_stage() {
   const uint32_t i = stage_next_;
-  stage_next_ = (i + 1) % c_.disk_staging;
-  const int32_t block = int32_t(c_.blocks + i);
-  end_reads([block](const Pending& p) { return p.stage == block; });
-  if (stage_ev_[i] && !m_->done(stage_ev_[i])) {
+  stage_next_ = (stage_next_ + 1) % c_.disk_staging;
+  const int32_t stage = int32_t(c_.blocks + i);
+  end_reads([stage](const Pending& p) { return p.stage == stage; });
+  if (stage_ev_[i] != nullptr && !m_->done(stage_ev_[i])) {
     m_->event_sync(stage_ev_[i]);
     ++st_.disk_stage_waits;
   }
-  return block;
+  return stage;
 }
 
 // ---- file reads in flight (disk_queue > 1) ----
@@ -293,11 +318,8 @@ void SlotCache::enter() {
 }
 
 void SlotCache::drain_pending(size_t n) {
-  end_reads([&n](const Pending&) {
-    if (n == 0) return false;
-    --n;
-    return true;
-  });
+  size_t left = n;
+  end_reads([&left](const Pending&) { return left != 0 && left-- != 0; });
 }
 
 void SlotCache::drain_demand() {
@@ -308,11 +330,12 @@ void SlotCache::drain_key(uint32_t k) {
   end_reads([k](const Pending& p) { return p.key == k; });
 }
 
-// The demand reads and the prefetch reads of units layer g routes (a wrong prediction's read keeps running).
+// The demand reads, and the prefetch reads of units layer g routes (a wrong prediction's read keeps running).
 void SlotCache::drain_layer(uint32_t g, const uint32_t* ids, uint32_t n) {
   const uint32_t first = key(g, 0);
-  end_reads([this, g, ids, n, first](const Pending& p) {
-    return !p.prefetch || (gated_of(p.key) == g && std::find(ids, ids + n, p.key - first) != ids + n);
+  end_reads([&](const Pending& p) {
+    if (!p.prefetch) return true;
+    return gated_of(p.key) == g && std::find(ids, ids + n, p.key - first) != ids + n;
   });
 }
 
@@ -321,35 +344,27 @@ void SlotCache::drain_layer(uint32_t g, const uint32_t* ids, uint32_t n) {
 // enqueued. The first failure is rethrown.
 void SlotCache::end_reads(const std::function<bool(const Pending&)>& pick) {
   if (pending_.empty()) return;
-  std::vector<uint8_t> picked(pending_.size());
-  for (size_t i = 0; i < pending_.size(); ++i) picked[i] = pick(pending_[i]) ? 1 : 0;
-  std::vector<Pending> ending;
-  ending.reserve(pending_.size());
-  size_t kept = 0;
-  for (size_t i = 0; i < pending_.size(); ++i) {
-    if (picked[i]) ending.push_back(pending_[i]);
-    else pending_[kept++] = pending_[i];
-  }
-  pending_.resize(kept);
-  std::exception_ptr first;
-  bool device_failed = false;
+  std::vector<Pending> ending, staying;
+  for (const Pending& p : pending_) (pick(p) ? ending : staying).push_back(p);
+  pending_.swap(staying);
+  std::exception_ptr failure;
+  bool device_down = false;
   for (size_t i = 0; i < ending.size(); ++i) {
     const Pending p = ending[i];
-    if (p.entry != entries_) {  // it ran while its fetch's caller went on
+    if (p.entry != entries_) {  // it ran on while its fetch's caller went on
       ++st_.disk_carried;
       st_.disk_carried_bytes += unit_bytes_;
     }
-    const auto t0 = std::chrono::steady_clock::now();
-    bool read_ok = true;
+    const auto t0 = Clock::now();
+    bool landed = true;
     try {
       st_.disk_read_ns += m_->read_end(p.handle);
     } catch (...) {
-      read_ok = false;
-      if (!first) first = std::current_exception();
+      landed = false;
+      if (!failure) failure = std::current_exception();
     }
-    st_.disk_wait_ns += uint64_t(
-        std::chrono::duration_cast<std::chrono::nanoseconds>(std::chrono::steady_clock::now() - t0).count());
-    if (!read_ok || device_failed) {
+    st_.disk_wait_ns += ns_since(t0);
+    if (!landed || device_down) {
       undo_pending(p);
       continue;
     }
@@ -358,32 +373,27 @@ void SlotCache::end_reads(const std::function<bool(const Pending&)>& pick) {
     try {
       finish_pending(p);
     } catch (...) {
-      if (!first) first = std::current_exception();
-      device_failed = true;  // (this record stays fetched, as a synchronous fetch whose copy failed)
+      if (!failure) failure = std::current_exception();
+      device_down = true;  // (this record stays fetched, as a synchronous fetch whose copy failed)
       ending.insert(ending.end(), pending_.begin(), pending_.end());
       pending_.clear();
     }
   }
-  if (first) std::rethrow_exception(first);
+  if (failure) std::rethrow_exception(failure);
 }
 
 // An ended read's device work: the copy from its staging buffer and the entry, the buffer's event, a prefetch's event.
 void SlotCache::finish_pending(const Pending& p) {
+  if (mut_ == kEntryBeforeCopy) publish(p.s, p.key, p.slot);  // test-only fault: the entry before its bytes
+  m_->h2d(p.s, p.slot, p.stage, p.key);
+  if (mut_ != kEntryBeforeCopy) publish(p.s, p.key, p.slot);
+  void*& stage_ev = stage_ev_[uint32_t(p.stage) - c_.blocks];  // the buffer is reusable once this copy landed
+  if (stage_ev == nullptr) stage_ev = event();
+  m_->record(stage_ev, p.s);
+  if (!p.prefetch) return;
   Entry& x = e_[p.key];
-  if (mut_ == kEntryBeforeCopy) {  // test-only fault: the entry before its bytes
-    publish(p.s, p.key, p.slot);
-    m_->h2d(p.s, p.slot, p.stage, p.key);
-  } else {
-    m_->h2d(p.s, p.slot, p.stage, p.key);
-    publish(p.s, p.key, p.slot);
-  }
-  void*& ev = stage_ev_[uint32_t(p.stage) - c_.blocks];  // the staging buffer is reusable once this copy landed
-  if (!ev) ev = event();
-  m_->record(ev, p.s);
-  if (p.prefetch) {
-    x.pf_done = event();
-    m_->record(x.pf_done, p.s);
-  }
+  x.pf_done = event();
+  m_->record(x.pf_done, p.s);
 }
 
 // A read that failed: the key goes back to its file, its slot to where it came from (a bank slot stays used for the
@@ -391,154 +401,113 @@ void SlotCache::finish_pending(const Pending& p) {
 void SlotCache::undo_pending(const Pending& p) {
   Entry& x = e_[p.key];
   const uint32_t g = gated_of(p.key);
-  table_[p.key] = -1;
   if (p.bank) {
+    table_[p.key] = -1;
     bank_key_[size_t(p.slot) - bank_first_] = kNil;
     banked_.erase(std::find(banked_.begin(), banked_.end(), p.key));
     --st_.bank_serves;
     --lc_[g].bank_serves;
   } else {
-    unlink(p.key);
-    --on_device_;
+    leave_device(p.key);
     coming_.erase(std::find(coming_.begin(), coming_.end(), p.key));
-    free_slots_.push_back(p.slot);
-    if (p.free_counted) --demand_free_used_;
+    free_slots_.give(p.slot);
+    demand_free_used_ -= p.free_counted ? 1 : 0;
   }
   x.home = Home::File;
   x.slot = -1;
   x.via_pf = x.used = false;
   ++on_file_;
-  if (p.prefetch) {
-    --st_.prefetched;
-    --lc_[g].prefetched;
-  } else {
-    --st_.fetched;
-    --lc_[g].fetched;
+  count_fetch(g, p.prefetch, -1);
+}
+
+// A file miss with the queue full: the completed reads end, then the oldest demand reads, then the oldest.
+void SlotCache::make_room_for_read() {
+  const size_t depth = std::max<uint32_t>(c_.disk_queue, 1);
+  if (pending_.size() < depth) return;
+  end_reads([this](const Pending& p) { return m_->read_done(p.handle); });
+  if (pending_.size() >= depth) {
+    size_t over = pending_.size() + 1 - depth;
+    end_reads([&over](const Pending& p) { return !p.prefetch && over != 0 && over-- != 0; });
   }
+  if (pending_.size() >= depth) drain_pending(pending_.size() + 1 - depth);
 }
 
-// ---- the recency list (head = most recently used) ----
-void SlotCache::unlink(uint32_t k) {
-  Entry& x = e_[k];
-  if (!x.listed) return;
-  if (x.prev != kNil) e_[x.prev].next = x.next;
-  else head_ = x.next;
-  if (x.next != kNil) e_[x.next].prev = x.prev;
-  else tail_ = x.prev;
-  x.prev = x.next = kNil;
-  x.listed = false;
-}
-
-void SlotCache::push_front(uint32_t k) {
-  Entry& x = e_[k];
-  x.prev = kNil;
-  x.next = head_;
-  if (head_ != kNil) e_[head_].prev = k;
-  else tail_ = k;
-  head_ = k;
-  x.listed = true;
-  if (c_.scored) {  // unique stamps, larger nearer the head (stamp_room keeps the counter far from wrapping)
-    if (stamp_ == UINT64_MAX) broken("the recency stamp counter wrapped");
-    x.lru_stamp = ++stamp_;
-  }
-}
-
-void SlotCache::stamp_room(const char* what) const {
-  if (c_.scored && stamp_ > kStampLimit)
-    fail(SS_E_BACKEND, std::string("device-gated: ") + what +
-                           ": the scored eviction's recency stamp counter is exhausted (reopen the context)");
-}
-
-void* SlotCache::event() {
-  if (!pool_.empty()) {
-    void* ev = pool_.back();
-    pool_.pop_back();
-    return ev;
-  }
-  void* ev = m_->event_create();
-  all_events_.push_back(ev);
-  return ev;
-}
-
-void SlotCache::publish(Mover::Stream s, uint32_t k, int32_t v) {
-  table_[k] = v;
-  m_->publish(s, k, v);
-}
-
+// ---- write-backs ----
 // Finished write-backs in submission order: the unit's home becomes its block and its slot is free; a discarded one
 // (the unit was resurrected) only returns its block.
 uint32_t SlotCache::collect() {
-  uint32_t n = 0;
-  while (!wbs_.empty()) {
-    Writeback& w = wbs_.front();
-    if (!m_->done(w.done)) break;
+  uint32_t done = 0;
+  for (; !wbs_.empty() && m_->done(wbs_.front().done); ++done) {
+    Writeback w = wbs_.front();
+    wbs_.pop_front();
     Entry& x = e_[w.key];
     x.wb_pending = false;
     if (w.discard) {
-      free_blocks_.push_back(w.block);
+      free_blocks_.give(w.block);
     } else {
       x.home = Home::Host;
       x.block = w.block;
       x.slot = -1;
-      hpush(w.key);
-      free_slots_.push_back(w.slot);
+      home_push(w.key);
+      free_slots_.give(w.slot);
     }
-    ++n;
     outstanding_ -= w.bytes;
     st_.wb_completed_bytes += w.bytes;
-    pool_.push_back(w.done);
-    wbs_.pop_front();
+    recycle(w.done);
   }
-  st_.writebacks_done += n;
-  return n;
+  st_.writebacks_done += done;
+  return done;
 }
 
 void SlotCache::submit_part(Deferred& d) {
   const uint32_t p = d.parts_done;
   m_->d2h(wb_stream_, d.slot, d.block, int32_t(p), d.key);
-  ++d.parts_done;
-  const uint64_t b = m_->part_bytes(p);
-  d.bytes += b;
-  outstanding_ += b;
-  st_.wb_issued_bytes += b;
+  d.parts_done = p + 1;
+  const uint64_t n = m_->part_bytes(p);
+  d.bytes += n;
+  outstanding_ += n;
+  st_.wb_issued_bytes += n;
 }
 
+// The deferred front, as far as it was submitted, becomes a write-back in flight (its completion event recorded).
 void* SlotCache::record_front(bool discard) {
-  Deferred& d = deferred_.front();
+  const Deferred& d = deferred_.front();
   void* ev = event();
   m_->record(ev, wb_stream_);
-  wbs_.push_back({d.key, d.slot, d.block, ev, discard, d.bytes});
+  wbs_.push_back(Writeback{d.key, d.slot, d.block, ev, discard, d.bytes});
   deferred_.pop_front();
   return ev;
 }
 
 void* SlotCache::finish_front() {
-  Deferred& d = deferred_.front();
-  while (d.parts_done < m_->parts()) submit_part(d);
+  for (Deferred& d = deferred_.front(); d.parts_done < m_->parts();) submit_part(d);
   return record_front(false);
 }
 
+// After layer g was served: the deferred write-backs' parts, within the layer's byte credit and the outstanding cap,
+// unless a later layer was already exported (ahead), never behind the last layer (the boundary's sync would wait).
 void SlotCache::issue_writebacks(uint32_t g, const std::function<bool()>& ahead) {
   enter();
   if (deferred_.empty()) {
     credit_ = 0;
     return;
   }
-  if (g + 1 >= gated()) return;  // never behind the last layer: the boundary's sync would wait for it
+  if (g + 1 >= gated()) return;
   const int64_t grant = int64_t(layer_bytes_);
   credit_ = std::min(credit_ + grant, grant);  // a debt carries over, unused credit does not
   st_.collected_mid += collect();
-  bool behind_ready = false;
-  while (credit_ > 0 && !deferred_.empty() && outstanding_ < max_outstanding_ && !(ahead && ahead())) {
-    if (wb_stream_ == Mover::kD2h && !behind_ready) {
+  bool fenced = false;  // the write-back stream waits for this layer's ready (once)
+  while (credit_ > 0 && !deferred_.empty() && outstanding_ < max_outstanding_) {
+    if (ahead && ahead()) break;
+    if (wb_stream_ == Mover::kD2h && !fenced) {
       m_->record(post_ready_ev_, Mover::kDem);
       m_->wait(Mover::kD2h, post_ready_ev_);
-      behind_ready = true;
+      fenced = true;
     }
     Deferred& d = deferred_.front();
     credit_ -= int64_t(m_->part_bytes(d.parts_done));
-    if (d.parts_done + 1 == m_->parts()) finish_front();
-    else submit_part(d);
+    if (d.parts_done + 1 < m_->parts()) submit_part(d);
+    else finish_front();
   }
 }
 
@@ -546,48 +515,52 @@ void SlotCache::issue_writebacks(uint32_t g, const std::function<bool()>& ahead)
 // the deferred front and wait for it) until a slot is free.
 void SlotCache::force_free_slot() {
   while (free_slots_.empty() && !deferred_.empty()) {
-    void* ev = nullptr;
-    for (const Writeback& w : wbs_)
-      if (!w.discard) {
-        ev = w.done;
-        break;
-      }
-    if (!ev) ev = finish_front();
+    const auto live = std::find_if(wbs_.begin(), wbs_.end(), [](const Writeback& w) { return !w.discard; });
+    void* ev = live != wbs_.end() ? live->done : finish_front();
     ++st_.wb_forced;
-    const auto t0 = std::chrono::steady_clock::now();
+    const auto t0 = Clock::now();
     m_->event_sync(ev);
-    st_.wb_forced_wait_ns += uint64_t(
-        std::chrono::duration_cast<std::chrono::nanoseconds>(std::chrono::steady_clock::now() - t0).count());
+    st_.wb_forced_wait_ns += ns_since(t0);
     st_.collected_mid += collect();
   }
 }
 
+// Between tokens: every copy settled and every write-back collected (the round, make-resident and reset need it).
+void SlotCache::settle_writebacks(const char* what) {
+  drain();
+  for (const Writeback& w : wbs_) m_->event_sync(w.done);
+  collect();
+  if (!wbs_.empty()) broken(std::string(what) + ": write-backs not collected");
+}
+
+// ---- banks ----
 // Bank g & 1 of the demand bank slots; a bank is reused two gated layers later, when the device has finished the
 // layer that used it before. The slot's previous unit goes back to its block and its entry is withdrawn first.
 int32_t SlotCache::bank_slot(uint32_t g) {
   const uint32_t b = g & 1u;
-  if (bank_seq_[b] != seq_ || bank_layer_[b] != g) {
+  if (bank_seq_[b] != seq_ || bank_layer_[b] != g) {  // the bank's first use by this layer this token
     bank_seq_[b] = seq_;
     bank_layer_[b] = g;
     bank_next_[b] = 0;
   }
   if (bank_next_[b] >= c_.bank_slots) return -1;
-  const uint32_t idx = b * c_.bank_slots + bank_next_[b]++;
-  const int32_t slot = int32_t(bank_first_ + idx);
-  const uint32_t old = bank_key_[idx];
-  if (old != kNil && e_[old].home == Home::Bank && e_[old].slot == slot) {
-    drain_key(old);  // (its read, were it still in flight, ends before the alias goes)
-    to_lower(old);  // its block, or (read from it) its file
-    publish(Mover::kDem, old, -1);
+  const uint32_t at = b * c_.bank_slots + bank_next_[b]++;
+  const int32_t slot = int32_t(bank_first_ + at);
+  const uint32_t prior = bank_key_[at];
+  if (prior != kNil && e_[prior].home == Home::Bank && e_[prior].slot == slot) {
+    drain_key(prior);  // (its read, were it still in flight, ends before the alias goes)
+    to_lower(prior);   // its block, or (read from it) its file
+    publish(Mover::kDem, prior, -1);
   }
-  bank_key_[idx] = kNil;
+  bank_key_[at] = kNil;
   return slot;
 }
 
+// ---- a token ----
 void SlotCache::begin_token(uint32_t seq, const std::vector<uint8_t>* run) {
   require(!run || run->size() == gated(), SS_E_INVALID, "device-gated: the exported layers do not cover the gated layers");
   enter();
-  if (run) std::copy(run->begin(), run->end(), run_.begin());
+  if (run) run_ = *run;
   else std::fill(run_.begin(), run_.end(), uint8_t(1));
   if (c_.scored) {  // the token's epoch (the first is 1); one token cannot push more than 2^40 stamps
     stamp_room("begin_token");
@@ -595,70 +568,58 @@ void SlotCache::begin_token(uint32_t seq, const std::vector<uint8_t>* run) {
     ++epoch_;
   }
   seq_ = seq;
-  pf_token_ = 0;
-  demand_free_used_ = 0;
+  pf_token_ = demand_free_used_ = 0;
   std::fill(pf_layer_.begin(), pf_layer_.end(), 0u);
   std::fill(layer_missed_.begin(), layer_missed_.end(), uint8_t(0));
   pred_.clear();
   pred_layer_ = kNil;
 }
 
+// An Evicting unit routed again: its slot still holds the bytes (a write-back only reads them). A deferred write-back
+// not yet begun is cancelled (its block free again); one partly submitted (only the front can be) or in flight is
+// kept as a discard. The unit is a device home again.
+bool SlotCache::resurrect(uint32_t k) {
+  Entry& x = e_[k];
+  const auto d = std::find_if(deferred_.begin(), deferred_.end(), [k](const Deferred& v) { return v.key == k; });
+  if (d != deferred_.end() && d->parts_done == 0) {
+    free_blocks_.give(d->block);
+    deferred_.erase(d);
+    x.wb_pending = false;
+    ++st_.wb_cancelled;
+    st_.wb_cancelled_bytes += unit_bytes_;
+  } else if (d != deferred_.end()) {
+    if (d != deferred_.begin()) broken("parts submitted behind the deferred front");
+    st_.wb_cancelled_bytes += unit_bytes_ - d->bytes;
+    record_front(true);
+  } else {
+    const auto w = std::find_if(wbs_.begin(), wbs_.end(), [k](const Writeback& v) { return v.key == k && !v.discard; });
+    if (w != wbs_.end()) w->discard = true;
+  }
+  x.home = Home::Device;
+  x.block = -1;
+  publish(Mover::kDem, k, x.slot);
+  touch(k);
+  ++on_device_;
+  ++st_.resurrected;
+  return true;
+}
+
 bool SlotCache::fetch(uint32_t g, uint32_t unit, bool prefetch) {
   const uint32_t k = key(g, unit);
   Entry& x = e_[k];
-  if (prefetch && (pf_layer_[g] >= c_.prefetch_per_layer || pf_token_ >= c_.prefetch_per_token)) return false;
-  if (prefetch && c_.no_admit) return false;  // (no_admit issues no prefetch)
-  switch (x.home) {
-    case Home::Coming:
-      drain_key(k);  // (its own prefetch read in flight: ended)
-      return false;
-    case Home::Device:
-    case Home::Bank:
-      return false;
-    case Home::Evicting: {  // resurrection: the slot still holds the bytes (a write-back only reads them)
-      for (auto it = deferred_.begin(); it != deferred_.end(); ++it) {
-        if (it->key != k) continue;
-        if (it->parts_done == 0) {  // nothing submitted: cancelled, its block free again
-          free_blocks_.push_back(it->block);
-          deferred_.erase(it);
-          x.wb_pending = false;
-          ++st_.wb_cancelled;
-          st_.wb_cancelled_bytes += unit_bytes_;
-        } else {  // partly submitted (only the front can be): recorded as a discard
-          if (it != deferred_.begin()) broken("parts submitted behind the deferred front");
-          st_.wb_cancelled_bytes += unit_bytes_ - it->bytes;
-          record_front(true);
-        }
-        x.home = Home::Device;
-        x.block = -1;
-        publish(Mover::kDem, k, x.slot);
-        push_front(k);
-        ++on_device_;
-        ++st_.resurrected;
-        return true;
-      }
-      for (Writeback& w : wbs_)
-        if (w.key == k && !w.discard) {
-          w.discard = true;
-          break;
-        }
-      x.home = Home::Device;
-      x.block = -1;
-      publish(Mover::kDem, k, x.slot);
-      push_front(k);
-      ++on_device_;
-      ++st_.resurrected;
-      return true;
-    }
-    case Home::Host:
-      break;
-    case Home::File:  // a file read below; a prefetch only with disk_prefetch
-      if (prefetch && !c_.disk_prefetch) return false;
-      break;
+  if (prefetch && (c_.no_admit || pf_layer_[g] >= c_.prefetch_per_layer || pf_token_ >= c_.prefetch_per_token))
+    return false;
+  if (x.home == Home::Coming) {
+    drain_key(k);  // (its own prefetch read in flight: ended)
+    return false;
   }
-  // a prefetch keeps the reserve free (pf_strict: the spare target's slots too)
+  if (x.home == Home::Device || x.home == Home::Bank) return false;
+  if (x.home == Home::Evicting) return resurrect(k);
+  if (x.home == Home::File && prefetch && !c_.disk_prefetch) return false;  // a file prefetch only with disk_prefetch
+  // where the unit goes: a free slot (a prefetch leaves the reserve free, pf_strict the spare target's slots too), else
+  // for a demand its layer's bank slot (no_admit: always)
   const size_t reserve =
-      prefetch ? (c_.pf_strict ? std::max<size_t>(c_.prefetch_reserve, c_.spare_target) : c_.prefetch_reserve) : 0u;
+      !prefetch ? 0u : c_.pf_strict ? std::max<size_t>(c_.prefetch_reserve, c_.spare_target) : c_.prefetch_reserve;
   int32_t slot = -1;
   bool bank = false, free_counted = false;
   if (c_.no_admit) {  // a demand: its layer's bank slot, released at the boundary, its home unchanged
@@ -672,81 +633,58 @@ bool SlotCache::fetch(uint32_t g, uint32_t unit, bool prefetch) {
   }
   const bool capped = !prefetch && pressure_ && demand_free_used_ >= pressure_free_;
   if (!bank && !prefetch && !capped && free_slots_.empty()) force_free_slot();
-  if (bank) {
-    // (no_admit: taken above)
-  } else if (!capped && free_slots_.size() > reserve) {
-    if (!prefetch) ++demand_free_used_;
-    free_counted = !prefetch;
-    slot = free_slots_.back();
-    free_slots_.pop_back();
-  } else if (prefetch) {
-    if (c_.pf_strict && free_slots_.size() > c_.prefetch_reserve) ++st_.pf_strict_refused;
-    return false;
-  } else {
-    slot = bank_slot(g);
-    if (slot >= 0) {
+  if (!bank) {
+    if (!capped && free_slots_.size() > reserve) {
+      free_counted = !prefetch;
+      demand_free_used_ += free_counted ? 1 : 0;
+      slot = free_slots_.take();
+    } else if (prefetch) {
+      if (c_.pf_strict && free_slots_.size() > c_.prefetch_reserve) ++st_.pf_strict_refused;
+      return false;
+    } else if ((slot = bank_slot(g)) >= 0) {
       bank = true;
     } else {  // more distinct misses than a bank holds: only an internal error gets here
       drain_pending();
       force_free_slot();
-      while (free_slots_.empty() && !wbs_.empty()) {
+      for (; free_slots_.empty() && !wbs_.empty(); ++st_.stalled) {
         m_->event_sync(wbs_.front().done);
         collect();
-        ++st_.stalled;
       }
       if (free_slots_.empty()) fail(SS_E_BACKEND, "device-gated: no free slot, no bank slot, no write-back to wait for");
-      slot = free_slots_.back();
-      free_slots_.pop_back();
+      slot = free_slots_.take();
     }
   }
   const Mover::Stream s = prefetch ? Mover::kPf : Mover::kDem;
   const bool from_file = x.home == Home::File;
   if (from_file) {  // its bytes from the file into a staging buffer, then the same copy once the read ended
-    const size_t depth = std::max<uint32_t>(c_.disk_queue, 1);
     try {
-      if (pending_.size() >= depth) {  // a full queue: the completed reads, then the oldest demand reads, then the oldest
-        end_reads([this](const Pending& p) { return m_->read_done(p.handle); });
-        if (pending_.size() >= depth) {
-          size_t n = pending_.size() + 1 - depth;
-          end_reads([&n](const Pending& p) {
-            if (n == 0 || p.prefetch) return false;
-            --n;
-            return true;
-          });
-        }
-        if (pending_.size() >= depth) drain_pending(pending_.size() + 1 - depth);
-      }
+      make_room_for_read();
       const int32_t stage = take_stage();
-      const auto t0 = std::chrono::steady_clock::now();
-      void* h = m_->read_begin(k, stage);
-      st_.disk_read_ns += uint64_t(
-          std::chrono::duration_cast<std::chrono::nanoseconds>(std::chrono::steady_clock::now() - t0).count());
-      if (!pending_.empty()) ++st_.disk_overlapped;
-      pending_.push_back({k, slot, stage, s, prefetch, bank, free_counted, h, entries_});
+      const auto t0 = Clock::now();
+      void* handle = m_->read_begin(k, stage);
+      st_.disk_read_ns += ns_since(t0);
+      st_.disk_overlapped += pending_.empty() ? 0 : 1;
+      pending_.push_back(Pending{k, slot, stage, s, prefetch, bank, free_counted, handle, entries_});
       st_.disk_max_in_flight = std::max<uint64_t>(st_.disk_max_in_flight, pending_.size());
     } catch (...) {  // nothing begun for this key: its slot goes back (a bank slot stays used, unpublished)
       if (!bank) {
-        free_slots_.push_back(slot);
-        if (free_counted) --demand_free_used_;
+        free_slots_.give(slot);
+        demand_free_used_ -= free_counted ? 1 : 0;
       }
       throw;
     }
     table_[k] = slot;  // the mirror now; the device's entry with the copy
     --on_file_;
   } else {
-    if (mut_ == kEntryBeforeCopy) {  // test-only fault: the entry before its bytes
-      publish(s, k, slot);
-      m_->h2d(s, slot, x.block, k);
-    } else {
-      m_->h2d(s, slot, x.block, k);
-      publish(s, k, slot);
-    }
-    hunlink(k);  // (a Host unit: out of the pinned recency list)
+    if (mut_ == kEntryBeforeCopy) publish(s, k, slot);  // test-only fault: the entry before its bytes
+    m_->h2d(s, slot, x.block, k);
+    if (mut_ != kEntryBeforeCopy) publish(s, k, slot);
+    home_erase(k);  // (a Host unit: out of the pinned recency list)
   }
   x.slot = slot;
   x.via_pf = prefetch;
   x.used = false;
-  if (prefetch && !from_file) {  // (a file read's: with its copy)
+  if (prefetch && !from_file) {  // (a file read's event comes with its copy)
     x.pf_done = event();
     m_->record(x.pf_done, s);
   }
@@ -754,33 +692,30 @@ bool SlotCache::fetch(uint32_t g, uint32_t unit, bool prefetch) {
     x.home = Home::Bank;
     bank_key_[size_t(slot) - bank_first_] = k;
     banked_.push_back(k);
-    ++st_.bank_serves;
-    ++lc_[g].bank_serves;
+    bump(g, &CacheStats::bank_serves, &LayerCounts::bank_serves);
   } else {
     x.home = Home::Coming;
     coming_.push_back(k);
-    push_front(k);
+    touch(k);
     ++on_device_;
   }
+  count_fetch(g, prefetch);
   if (prefetch) {
-    ++st_.prefetched;
-    ++lc_[g].prefetched;
     ++pf_layer_[g];
     ++pf_token_;
-  } else {
-    ++st_.fetched;
-    ++lc_[g].fetched;
   }
   if (from_file && c_.disk_queue <= 1) drain_pending();  // synchronous reads: the copy now
   return true;
 }
 
 void SlotCache::cover(uint32_t g, uint32_t unit) {
-  Entry& x = e_[key(g, unit)];
-  // only this key's copy lands before the ready: its read ends first if in flight (a file prefetch's event comes
-  // with its copy), the wait is on its own event
-  if (x.home == Home::Coming && x.via_pf && mut_ != kNoCover) drain_key(key(g, unit));
-  if (x.home == Home::Coming && x.via_pf && x.pf_done && mut_ != kNoCover) {
+  const uint32_t k = key(g, unit);
+  Entry& x = e_[k];
+  if (mut_ == kNoCover || x.home != Home::Coming || !x.via_pf) return;
+  // only this key's copy lands before the ready: its read ends first if in flight (a file prefetch's event comes with
+  // its copy), the wait is on its own event
+  drain_key(k);
+  if (x.home == Home::Coming && x.via_pf && x.pf_done) {
     m_->wait(Mover::kDem, x.pf_done);
     ++st_.covered_waits;
   }
@@ -790,26 +725,18 @@ void SlotCache::use(uint32_t g, uint32_t unit, bool was_miss) {
   enter();
   const uint32_t k = key(g, unit);
   Entry& x = e_[k];
-  ++st_.lookups;
-  ++lc_[g].lookups;
+  bump(g, &CacheStats::lookups, &LayerCounts::lookups);
   if (was_miss) {
-    ++st_.misses;
-    ++lc_[g].misses;
-    if (!layer_missed_[g]) {
-      layer_missed_[g] = 1;
-      ++st_.miss_layers;
-    }
+    bump(g, &CacheStats::misses, &LayerCounts::misses);
+    if (!layer_missed_[g]) ++st_.miss_layers;  // (the layer's first miss this token)
+    layer_missed_[g] = 1;
   }
   if (c_.scored) x.demand_epoch = epoch_;  // a routed use (never a prefetch, a resurrection or a seed)
   if (x.via_pf && !x.used) {
     x.used = true;
-    ++st_.prefetch_used;
-    ++lc_[g].prefetch_used;
+    bump(g, &CacheStats::prefetch_used, &LayerCounts::prefetch_used);
   }
-  if (x.listed) {
-    unlink(k);
-    push_front(k);
-  }
+  if (recent_.has(k)) touch(k);
 }
 
 void SlotCache::serve_demand(uint32_t g, const uint32_t* ids, uint32_t n, uint64_t mask) {
@@ -822,40 +749,38 @@ void SlotCache::serve_demand(uint32_t g, const uint32_t* ids, uint32_t n, uint64
   if (mask) m_->diag_mark(g, 0);
   // masked occurrences in export order: a repeated id is fetched at its first occurrence, covered at the others
   for (uint32_t i = 0; i < n; ++i) {
-    if (!(mask >> i & 1u)) continue;
+    if (!((mask >> i) & 1u)) continue;
     const Home h = e_[key(g, ids[i])].home;
-    if (h == Home::Device || h == Home::Coming || h == Home::Bank) {
-      cover(g, ids[i]);
-      ++st_.covered;
-    } else {
+    if (h != Home::Device && h != Home::Coming && h != Home::Bank) {
       fetch(g, ids[i], false);
+      continue;
     }
+    cover(g, ids[i]);
+    ++st_.covered;
   }
   drain_layer(g, ids, n);  // this layer's copies and entries (its demand reads, the prefetch reads it routes)
-  if (mask) {
-    drain_demand();  // (the ready follows every demand read's copy and entry)
-    m_->ready(g, seq_);
-    m_->diag_mark(g, 1);
-  }
+  if (!mask) return;
+  drain_demand();  // (the ready follows every demand read's copy and entry)
+  m_->ready(g, seq_);
+  m_->diag_mark(g, 1);
 }
 
 void SlotCache::serve_use(uint32_t g, const uint32_t* ids, uint32_t n, uint64_t mask) {
   enter();
-  const bool have_pred = pred_layer_ == g;
+  const bool predicted = pred_layer_ == g;
   uniq_.assign(ids, ids + n);
   std::sort(uniq_.begin(), uniq_.end());
   uniq_.erase(std::unique(uniq_.begin(), uniq_.end()), uniq_.end());
   if (c_.scored) score_history(g);  // (the union saved before a prediction reuses uniq_)
   for (uint32_t id : uniq_) {  // placement rounds: the tokens that routed the unit since the last round
-    uint32_t& h = rhits_[key(g, id)];
-    if (h != UINT32_MAX) ++h;
+    uint32_t& hits = rhits_[key(g, id)];
+    hits += hits != UINT32_MAX ? 1 : 0;
   }
   for (uint32_t id : uniq_) {
-    bool miss = false;
-    for (uint32_t i = 0; i < n; ++i)
-      if (ids[i] == id && (mask >> i & 1u)) miss = true;
-    use(g, id, miss);
-    if (have_pred && std::find(pred_.begin(), pred_.end(), id) != pred_.end()) ++st_.predicted_true;
+    bool missed = false;
+    for (uint32_t i = 0; i < n && !missed; ++i) missed = ids[i] == id && ((mask >> i) & 1u);
+    use(g, id, missed);
+    if (predicted && std::find(pred_.begin(), pred_.end(), id) != pred_.end()) ++st_.predicted_true;
   }
   pred_.clear();
   pred_layer_ = kNil;
@@ -870,237 +795,217 @@ void SlotCache::serve_prediction(uint32_t g_next, const uint32_t* pred, uint32_t
   const uint32_t nu = units(g_next);
   uniq_.clear();
   for (uint32_t i = 0; i < n; ++i) {
-    if (pred[i] >= nu) {
-      ++st_.pred_invalid;
-      continue;
-    }
-    if (std::find(uniq_.begin(), uniq_.end(), pred[i]) == uniq_.end()) uniq_.push_back(pred[i]);
+    if (pred[i] >= nu) ++st_.pred_invalid;
+    else if (std::find(uniq_.begin(), uniq_.end(), pred[i]) == uniq_.end()) uniq_.push_back(pred[i]);
   }
   st_.predicted += uniq_.size();
-  pred_.assign(uniq_.begin(), uniq_.end());
+  pred_ = uniq_;
   pred_layer_ = g_next;
   for (uint32_t id : pred_) fetch(g_next, id, true);
 }
 
+// ---- the boundary ----
 void SlotCache::end_token(const std::vector<uint32_t>& keep, uint32_t rows) {
   drain_pending();  // the end of the token: no read in flight while its streams sync and victims are chosen
   m_->sync(Mover::kDem);
   m_->sync(Mover::kPf);
-  std::vector<uint8_t> kept;
+  std::vector<uint8_t> held;
   if (!keep.empty()) {
-    kept.assign(keys_, 0);
+    held.assign(keys_, 0);
     for (uint32_t k : keep)
-      if (k < keys_) kept[k] = 1;
+      if (k < keys_) held[k] = 1;
   }
-  auto keep_k = [&](uint32_t k) { return !kept.empty() && kept[k]; };
-  for (uint32_t k : coming_) {  // arrivals become device homes; their source blocks are free
+  auto is_held = [&held](uint32_t k) { return !held.empty() && held[k]; };
+  // (1) the token's arrivals become device homes, their source blocks free (or kept as the inclusive share's clean
+  // copies); pf_revert: an unused prefetch goes back to its source block at the pinned recency tail (or, read from it,
+  // its file), its slot free, its entry withdrawn by the upload below
+  for (uint32_t k : coming_) {
     Entry& x = e_[k];
     if (x.home != Home::Coming) continue;
-    if (c_.pf_revert && x.via_pf && !x.used && !keep_k(k)) {
-      // an unused prefetch goes back: to its source block (still holding the bytes) at the pinned recency tail, or
-      // (read from it) to its file; no write-back, and the table upload below withdraws its entry
+    recycle(x.pf_done);
+    if (c_.pf_revert && x.via_pf && !x.used && !is_held(k)) {
       ++st_.pf_reverted;
       st_.pf_revert_bytes += unit_bytes_;
-      free_slots_.push_back(x.slot);
+      free_slots_.give(x.slot);
       to_lower(k, true);
-      table_[k] = -1;
-      unlink(k);
-      --on_device_;
+      leave_device(k);
       x.via_pf = false;
-      if (x.pf_done) {
-        pool_.push_back(x.pf_done);
-        x.pf_done = nullptr;
-      }
       continue;
     }
     x.home = Home::Device;
     x.via_pf = false;
-    if (x.pf_done) {
-      pool_.push_back(x.pf_done);
-      x.pf_done = nullptr;
-    }
-    if (x.block >= 0) {  // (a unit read from its file holds none)
-      if (backed_ < c_.inclusive) {  // inclusive share: the source block stays as a clean copy of the slot's bytes
-        x.backed = true;
-        ++backed_;
-        ++st_.inclusive_kept;
-      } else {
-        free_blocks_.push_back(x.block);
-        x.block = -1;
-      }
+    if (x.block < 0) continue;  // (read from its file: no block)
+    if (backed_ < c_.inclusive) {
+      x.backed = true;
+      ++backed_;
+      ++st_.inclusive_kept;
+    } else {
+      free_blocks_.give(x.block);
+      x.block = -1;
     }
   }
   coming_.clear();
-  for (uint32_t k : banked_) {  // bank units go back to their blocks (or, read from it, their file)
+  // (2) bank units go back to their blocks (or, read from it, their file)
+  for (uint32_t k : banked_) {
     Entry& x = e_[k];
     if (x.home == Home::Bank) {
       to_lower(k);
       table_[k] = -1;
     }
-    if (x.pf_done) {
-      pool_.push_back(x.pf_done);
-      x.pf_done = nullptr;
-    }
+    recycle(x.pf_done);
     x.via_pf = false;
   }
   banked_.clear();
   std::fill(bank_key_.begin(), bank_key_.end(), kNil);
   bank_seq_[0] = bank_seq_[1] = 0;
   bank_layer_[0] = bank_layer_[1] = kNil;
+  // (3) victims until free slots + write-backs still to free one reach the spare target
   collect();
-  size_t pending = deferred_.size();
-  for (const Writeback& w : wbs_) pending += w.discard ? 0u : 1u;
-  const size_t base = free_slots_.size() + pending;
+  size_t freeing = deferred_.size();
+  for (const Writeback& w : wbs_) freeing += w.discard ? 0u : 1u;
+  const size_t have = free_slots_.size() + freeing;
   victims_.clear();
-  size_t got = 0;
-  bool short_blocks = false;
+  size_t taken = 0;
+  bool out_of_blocks = false;
   auto eligible = [&](uint32_t k) {
     const Entry& x = e_[k];
-    return x.home == Home::Device && !x.wb_pending && !(kept.size() && kept[k]);
+    return x.home == Home::Device && !x.wb_pending && !is_held(k);
   };
-  auto accept = [&](uint32_t k) {
+  // A victim leaves without a copy when its block holds a clean copy, when clean_evict drops it to its file, or (file
+  // tier) when no block can be freed by dropping a pinned unit to its file; else it takes a free block and its
+  // write-back is issued below. No block at all: the boundary stops short.
+  auto evict = [&](uint32_t k) {
     Entry& x = e_[k];
-    // a clean copy (its block is its home again) or, file tier with no block to free, its file: no copy; a pinned
-    // unit dropped to its file frees a block first when none is free (clean_evict: none is dropped for it)
     const bool clean = !x.backed && clean_now();
-    if (x.backed || clean || (free_blocks_.empty() && !drop_host_lru() && c_.disk_tier)) {
-      if (x.backed) ++st_.inclusive_drops;
-      else ++st_.disk_discards;
-      if (clean) count_clean();
-      unlink(k);
-      --on_device_;
-      free_slots_.push_back(x.slot);
-      to_lower(k);
-      table_[k] = -1;
-      ++st_.evicted;
-      ++lc_[gated_of(k)].evicted;
-      ++got;
-      return true;
-    }
-    if (free_blocks_.empty()) {
+    const bool no_copy =
+        x.backed || clean || (free_blocks_.empty() && !drop_host_lru() && c_.disk_tier);
+    if (!no_copy && free_blocks_.empty()) {
       ++st_.evict_short;
-      short_blocks = true;
+      out_of_blocks = true;
       return false;
     }
-    const int32_t b = free_blocks_.back();
-    free_blocks_.pop_back();
-    unlink(k);
-    --on_device_;
+    ++taken;
+    if (no_copy) {
+      ++(x.backed ? st_.inclusive_drops : st_.disk_discards);
+      if (clean) count_clean();
+      free_slots_.give(x.slot);
+      leave_device(k);
+      to_lower(k);
+      count_evicted(k);
+      return true;
+    }
+    x.block = free_blocks_.take();
+    leave_device(k);
     x.home = Home::Evicting;
-    x.block = b;
     x.wb_pending = true;
-    table_[k] = -1;
     victims_.push_back(k);
-    ++got;
     return true;
   };
-  // scored eviction: the lowest scores among the eligible units, when every gated layer was closed this token (a
-  // layer the token did not export is closed here from its unchanged history); else the recency tail
-  const bool select = !c_.no_admit;  // (no_admit: nothing was admitted, no boundary evicts)
-  const bool want_score = select && c_.scored && (!c_.scored_auto || rows > 1);
-  for (uint32_t g = 0; c_.scored && g < gated(); ++g)
-    if (!run_[g]) sc_[g].list_epoch = epoch_;
-  bool by_score = want_score;
-  for (uint32_t g = 0; by_score && g < gated(); ++g) by_score = sc_[g].list_epoch == epoch_;
+  // scored eviction: the lowest scores among the eligible units, when every gated layer was closed this token (a layer
+  // the token did not export is closed here from its unchanged history); else the recency tail
+  const bool selecting = !c_.no_admit;  // (no_admit: nothing was admitted, no boundary evicts)
+  const bool want_score = selecting && c_.scored && (!c_.scored_auto || rows > 1);
+  if (c_.scored)
+    for (uint32_t g = 0; g < gated(); ++g)
+      if (!run_[g]) sc_[g].list_epoch = epoch_;
+  const bool by_score =
+      want_score && std::all_of(sc_.begin(), sc_.end(), [this](const LayerScore& h) { return h.list_epoch == epoch_; });
   if (want_score && !by_score) ++st_.score_fallbacks;
   if (by_score) {
-    const auto t0 = std::chrono::steady_clock::now();
-    select_scored(c_.spare_target > base ? c_.spare_target - base : 0, eligible);
+    const auto t0 = Clock::now();
+    select_scored(c_.spare_target > have ? c_.spare_target - have : 0, eligible);
     for (const ScoreCand& cd : select_heap_) {
-      if (!accept(cd.key)) break;
+      if (!evict(cd.key)) break;
       ++st_.scored_victims;
     }
-    st_.score_ns += uint64_t(
-        std::chrono::duration_cast<std::chrono::nanoseconds>(std::chrono::steady_clock::now() - t0).count());
-  } else if (select) {
-    for (uint32_t k = tail_; k != kNil && base + got < c_.spare_target;) {
-      const uint32_t prev = e_[k].prev;
-      if (eligible(k) && !accept(k)) break;
-      k = prev;
+    st_.score_ns += ns_since(t0);
+  } else if (selecting) {
+    for (uint32_t k = recent_.back(); k != kNil && have + taken < c_.spare_target;) {
+      const uint32_t newer = recent_.newer(k);  // (k may leave the list)
+      if (eligible(k) && !evict(k)) break;
+      k = newer;
     }
   }
-  if (select && pressure_ && pressure_recent_ && !short_blocks) {  // test pressure: the most recent ones too
+  if (selecting && pressure_ && pressure_recent_ && !out_of_blocks) {  // test pressure: the most recent ones too
     uint32_t n = 0;
-    for (uint32_t k = head_; k != kNil && n < pressure_recent_;) {
-      const uint32_t next = e_[k].next;
+    for (uint32_t k = recent_.front(); k != kNil && n < pressure_recent_;) {
+      const uint32_t older = recent_.older(k);
       if (eligible(k)) {
-        if (!accept(k)) break;
+        if (!evict(k)) break;
         ++n;
       }
-      k = next;
+      k = older;
     }
   }
+  // (4) the table, then the write-backs behind it: deferred ones carried by the larger of this and the last boundary's
+  // evictions (the older ones flushed now), or issued at once on the write-back stream
   const size_t n_evict = victims_.size();
-  m_->upload_table(table_.data(), keys_);  // the table first, then the write-backs behind it
-  const size_t n_old = deferred_.size(), carry = std::max(n_evict, prev_evict_);
-  const size_t n_flush = n_old > carry ? n_old - carry : 0;
+  m_->upload_table(table_.data(), keys_);
+  const size_t carry = std::max(n_evict, prev_evict_);
+  const size_t n_flush = deferred_.size() > carry ? deferred_.size() - carry : 0;
   prev_evict_ = n_evict;
   credit_ = 0;
-  for (size_t i = 0; c_.wb_defer && i < n_evict; ++i) {
-    const uint32_t k = victims_[i];
-    deferred_.push_back({k, e_[k].slot, e_[k].block, 0, 0});
-    ++st_.wb_deferred;
-    ++st_.evicted;
-    ++lc_[gated_of(k)].evicted;
-  }
-  const uint64_t issued0 = st_.wb_issued_bytes;
+  if (c_.wb_defer)
+    for (uint32_t k : victims_) {
+      deferred_.push_back(Deferred{k, e_[k].slot, e_[k].block, 0, 0});
+      ++st_.wb_deferred;
+      count_evicted(k);
+    }
+  const uint64_t issued_before = st_.wb_issued_bytes;
   for (size_t i = 0; i < n_flush; ++i) finish_front();
   st_.wb_boundary_flushed += n_flush;
-  st_.wb_boundary_flushed_bytes += st_.wb_issued_bytes - issued0;
-  for (size_t i = 0; !c_.wb_defer && i < n_evict; ++i) {
-    const uint32_t k = victims_[i];
-    const Entry& x = e_[k];
-    m_->d2h(Mover::kD2h, x.slot, x.block, -1, k);
-    void* ev = event();
-    m_->record(ev, Mover::kD2h);
-    wbs_.push_back({k, x.slot, x.block, ev, false, unit_bytes_});
-    outstanding_ += unit_bytes_;
-    st_.wb_issued_bytes += unit_bytes_;
-    ++st_.evicted;
-    ++lc_[gated_of(k)].evicted;
-  }
+  st_.wb_boundary_flushed_bytes += st_.wb_issued_bytes - issued_before;
+  if (!c_.wb_defer)
+    for (uint32_t k : victims_) {
+      const Entry& x = e_[k];
+      m_->d2h(Mover::kD2h, x.slot, x.block, -1, k);
+      void* ev = event();
+      m_->record(ev, Mover::kD2h);
+      wbs_.push_back(Writeback{k, x.slot, x.block, ev, false, unit_bytes_});
+      outstanding_ += unit_bytes_;
+      st_.wb_issued_bytes += unit_bytes_;
+      count_evicted(k);
+    }
   ++st_.tokens;
 }
 
 // ---- scored eviction ----
-// Layer g's union of this token (uniq_, sorted) against the previous token's: every (r in the previous union, e in
-// this one) cell takes one saturating increment and its row sum with it; the union enters the window ring (the oldest
-// leaves it once 16 are held) and becomes the previous one.
+// Layer g's union of this token (uniq_, sorted) against the previous token's: every (r in the previous union, e in this
+// one) cell takes one saturating increment and its row sum with it; the union enters the window ring (the oldest
+// leaves once 16 are held) and becomes the previous one.
 void SlotCache::score_history(uint32_t g) {
-  LayerScore& l = sc_[g];
+  LayerScore& h = sc_[g];
   const uint32_t n = units(g);
   require(uniq_.size() <= c_.max_ids, SS_E_BACKEND, "device-gated: a score union above max ids");
-  l.cur.assign(uniq_.begin(), uniq_.end());
-  l.served = epoch_;
-  for (uint32_t r : l.prev) {
-    uint32_t* row = l.T.data() + size_t(r) * n;
-    for (uint32_t e : l.cur) {
+  h.cur = uniq_;
+  h.served = epoch_;
+  for (uint32_t r : h.prev) {
+    uint32_t* row = &h.T[size_t(r) * n];
+    for (uint32_t e : h.cur) {
       if (row[e] == UINT32_MAX) {
         ++st_.score_saturated;
-        continue;
+      } else {
+        row[e] += 1;
+        h.rowsum[r] += 1;
       }
-      ++row[e];
-      ++l.rowsum[r];
     }
   }
-  if (l.ring_n == kWindow) {
-    const uint32_t* old = l.ring.data() + size_t(l.ring_head) * c_.max_ids;
-    for (uint32_t i = 0; i < l.ring_len[l.ring_head]; ++i) --l.cnt[old[i]];
-    l.ring_head = (l.ring_head + 1) % kWindow;
-    --l.ring_n;
+  const size_t width = c_.max_ids;
+  if (h.ring_n == kWindow) {  // the oldest union leaves the window
+    for (uint32_t i = 0; i < h.ring_len[h.ring_head]; ++i) h.cnt[h.ring[h.ring_head * width + i]] -= 1;
+    h.ring_head = (h.ring_head + 1) % kWindow;
+    h.ring_n -= 1;
   }
-  const uint32_t at = (l.ring_head + l.ring_n) % kWindow;
-  std::copy(l.cur.begin(), l.cur.end(), l.ring.begin() + ptrdiff_t(size_t(at) * c_.max_ids));
-  l.ring_len[at] = uint8_t(l.cur.size());
-  ++l.ring_n;
-  for (uint32_t e : l.cur) ++l.cnt[e];
-  l.prev.assign(l.cur.begin(), l.cur.end());
+  const uint32_t at = (h.ring_head + h.ring_n++) % kWindow;
+  std::copy(h.cur.begin(), h.cur.end(), h.ring.begin() + std::ptrdiff_t(at * width));
+  h.ring_len[at] = uint8_t(h.cur.size());
+  for (uint32_t e : h.cur) h.cnt[e] += 1;
+  h.prev = h.cur;
 }
 
 void SlotCache::score_layer(uint32_t g) {
   enter();
-  if (!c_.scored || g >= gated() || sc_[g].served != epoch_) return;  // (not served: the boundary falls back)
-  sc_[g].list_epoch = epoch_;
+  if (c_.scored && g < gated() && sc_[g].served == epoch_) sc_[g].list_epoch = epoch_;  // (not served: fall back)
 }
 
 // Unit u of layer g with cur = this token's union: N = sum over r in cur of T[r][u], D = sum over cur of the row
@@ -1108,16 +1013,17 @@ void SlotCache::score_layer(uint32_t g) {
 // S = w_t P + w_f F + w_r Rec in unsigned floor arithmetic (N <= D, so P <= |cur| << 16 and S < 2^33). With a cutoff
 // that F and Rec alone cannot beat, the transition rows are not read.
 SlotCache::ScoreCand SlotCache::score_candidate(uint32_t g, uint32_t u, uint64_t D, const ScoreCand* cutoff) const {
-  const LayerScore& l = sc_[g];
-  const Entry& x = e_[base_[g] + u];
-  const uint64_t F = (uint64_t(l.cnt[u]) << 16) / kWindow;
-  const uint64_t R = (uint64_t(1) << 16) / (1 + (epoch_ - x.demand_epoch));
-  ScoreCand cd{uint64_t(c_.w_freq) * F + uint64_t(c_.w_rec) * R, x.demand_epoch, x.lru_stamp, base_[g] + u};
-  if (cutoff && !cand_less(cd, *cutoff)) return cd;
-  uint64_t N = 0;
-  for (uint32_t r : l.cur) N += l.T[size_t(r) * units(g) + u];
-  const uint64_t P = ((uint64_t(l.cur.size()) * N) << 16) / std::max<uint64_t>(1, D);
-  cd.s += uint64_t(c_.w_trans) * P;
+  const LayerScore& h = sc_[g];
+  const uint32_t k = base_[g] + u;
+  const Entry& x = e_[k];
+  const uint64_t freq = (uint64_t(h.cnt[u]) << 16) / kWindow;
+  const uint64_t rec = (uint64_t(1) << 16) / (1 + (epoch_ - x.demand_epoch));
+  ScoreCand cd{uint64_t(c_.w_freq) * freq + uint64_t(c_.w_rec) * rec, x.demand_epoch, x.lru_stamp, k};
+  if (cutoff != nullptr && !cand_less(cd, *cutoff)) return cd;
+  uint64_t hits = 0;
+  const size_t n = units(g);
+  for (uint32_t r : h.cur) hits += h.T[r * n + u];
+  cd.s += uint64_t(c_.w_trans) * (((uint64_t(h.cur.size()) * hits) << 16) / std::max<uint64_t>(D, 1));
   return cd;
 }
 
@@ -1125,50 +1031,50 @@ SlotCache::ScoreCand SlotCache::score_candidate(uint32_t g, uint32_t u, uint64_t
 // max-heap over all layers, scored from each layer's current union, epochs and stamps.
 void SlotCache::select_scored(size_t need, const std::function<bool(uint32_t)>& eligible, bool count) {
   select_heap_.clear();
-  for (uint32_t g = 0; need && g < gated(); ++g) {
-    uint64_t D = 0;
-    for (uint32_t r : sc_[g].cur) D += sc_[g].rowsum[r];
-    if (count) ++st_.score_layers;
+  auto& heap = select_heap_;
+  for (uint32_t g = 0; need != 0 && g < gated(); ++g) {
+    uint64_t denom = 0;
+    for (uint32_t r : sc_[g].cur) denom += sc_[g].rowsum[r];
+    st_.score_layers += count ? 1 : 0;
     for (uint32_t u = 0; u < units(g); ++u) {
       if (!eligible(base_[g] + u)) continue;
-      if (count) ++st_.score_candidates;
-      const ScoreCand cd = score_candidate(g, u, D, select_heap_.size() == need ? &select_heap_.front() : nullptr);
-      if (select_heap_.size() < need) {
-        select_heap_.push_back(cd);
-        std::push_heap(select_heap_.begin(), select_heap_.end(), cand_less);
-      } else if (cand_less(cd, select_heap_.front())) {
-        std::pop_heap(select_heap_.begin(), select_heap_.end(), cand_less);
-        select_heap_.back() = cd;
-        std::push_heap(select_heap_.begin(), select_heap_.end(), cand_less);
+      st_.score_candidates += count ? 1 : 0;
+      const bool full = heap.size() == need;
+      const ScoreCand cd = score_candidate(g, u, denom, full ? &heap.front() : nullptr);
+      if (!full) {
+        heap.push_back(cd);
+        std::push_heap(heap.begin(), heap.end(), cand_less);
+      } else if (cand_less(cd, heap.front())) {  // the worst kept one leaves
+        std::pop_heap(heap.begin(), heap.end(), cand_less);
+        heap.back() = cd;
+        std::push_heap(heap.begin(), heap.end(), cand_less);
       }
     }
   }
-  std::sort_heap(select_heap_.begin(), select_heap_.end(), cand_less);
+  std::sort_heap(heap.begin(), heap.end(), cand_less);
 }
 
 // The open state of every score table: the profile's counts (or zeros), an empty window, no union, epoch 0, the
 // open's stamps.
 void SlotCache::reset_score() {
   for (uint32_t g = 0; g < uint32_t(sc_.size()); ++g) {
-    LayerScore& l = sc_[g];
-    const uint32_t n = units(g);
-    if (l.open_T.empty()) std::fill(l.T.begin(), l.T.end(), 0u);
-    else std::copy(l.open_T.begin(), l.open_T.end(), l.T.begin());
-    for (uint32_t r = 0; r < n; ++r) {
-      uint64_t sum = 0;
-      for (uint32_t e = 0; e < n && !l.open_T.empty(); ++e) sum += l.T[size_t(r) * n + e];
-      l.rowsum[r] = sum;
-    }
-    std::fill(l.cnt.begin(), l.cnt.end(), uint16_t(0));
-    std::fill(l.ring.begin(), l.ring.end(), 0u);
-    std::fill(l.ring_len.begin(), l.ring_len.end(), uint8_t(0));
-    l.ring_head = l.ring_n = 0;
-    l.prev.clear();
-    l.cur.clear();
-    l.served = l.list_epoch = 0;
+    LayerScore& h = sc_[g];
+    const size_t n = units(g);
+    if (h.open_T.empty()) std::fill(h.T.begin(), h.T.end(), 0u);
+    else h.T = h.open_T;
+    for (size_t r = 0; r < n; ++r)
+      h.rowsum[r] = h.open_T.empty() ? 0 : std::accumulate(h.T.begin() + std::ptrdiff_t(r * n),
+                                                           h.T.begin() + std::ptrdiff_t((r + 1) * n), uint64_t(0));
+    std::fill(h.cnt.begin(), h.cnt.end(), uint16_t(0));
+    std::fill(h.ring.begin(), h.ring.end(), 0u);
+    std::fill(h.ring_len.begin(), h.ring_len.end(), uint8_t(0));
+    h.ring_head = h.ring_n = 0;
+    h.prev.clear();
+    h.cur.clear();
+    h.served = h.list_epoch = 0;
   }
   epoch_ = 0;
-  stamp_ = open_stamp_;
+  stamp_ = open_.stamp;
 }
 
 void SlotCache::set_policy(uint32_t policy) {
@@ -1181,30 +1087,33 @@ void SlotCache::set_policy(uint32_t policy) {
   c_.scored_auto = policy == 2;
   reset_score();
   for (Entry& x : e_) x.demand_epoch = x.lru_stamp = 0;
-  stamp_ = 0;
-  for (uint32_t k = tail_; k != kNil; k = e_[k].prev) e_[k].lru_stamp = ++stamp_;
+  stamp_ = 0;  // the stamps follow the recency order from the back
+  for (uint32_t k = recent_.back(); k != kNil; k = recent_.newer(k)) e_[k].lru_stamp = ++stamp_;
 }
 
 void SlotCache::load_counts(const std::vector<std::vector<uint32_t>>& cells) {
   require(c_.scored && cells.size() == sc_.size(), SS_E_INVALID, "device-gated: a score profile needs policy SCORED");
   for (uint32_t g = 0; g < gated(); ++g) {
-    LayerScore& l = sc_[g];
-    const uint32_t n = units(g);
-    require(cells[g].size() == size_t(n) * n, SS_E_INVALID, "device-gated: a profile layer is not units^2 counts");
-    l.T = cells[g];
-    for (uint32_t r = 0; r < n; ++r) {
-      uint64_t sum = 0;
-      for (uint32_t e = 0; e < n; ++e) sum += l.T[size_t(r) * n + e];
-      l.rowsum[r] = sum;
-    }
-    l.open_T = l.T;  // the reset_open state
+    const size_t n = units(g);
+    require(cells[g].size() == n * n, SS_E_INVALID, "device-gated: a profile layer is not units^2 counts");
+    LayerScore& h = sc_[g];
+    h.T = cells[g];
+    for (size_t r = 0; r < n; ++r)
+      h.rowsum[r] = std::accumulate(h.T.begin() + std::ptrdiff_t(r * n), h.T.begin() + std::ptrdiff_t((r + 1) * n),
+                                    uint64_t(0));
+    h.open_T = h.T;  // the reset_open state
   }
 }
 
 // ---- kept-resident layers (ss_dg_make_resident) ----
+// Every refusal comes first (ids, capacity, blocks), then the cache settles, then: prefetches of the layer already
+// landed are admitted; victims are chosen for the units still to copy in (scores when scored, else the recency tail);
+// each unit goes into a free slot, evicting victims (a clean copy or a drop to a file costs nothing, a dirty one is
+// written back first) when none is free; a pinned unit is copied from its block, a file unit read through the staging
+// buffers (reads in flight up to the queue depth). The units copied in become the most recent, in the caller's order.
 SlotCache::ResidentResult SlotCache::make_resident(uint32_t g, const std::vector<uint32_t>& ids,
                                                    const std::vector<uint32_t>& other_kept) {
-  const auto t0 = std::chrono::steady_clock::now();
+  const auto t0 = Clock::now();
   require(g < gated(), SS_E_INVALID, "ss_dg_make_resident: gated layer out of range");
   std::vector<uint8_t> want(keys_, 0), other(keys_, 0);
   for (uint32_t u : ids) {
@@ -1213,58 +1122,51 @@ SlotCache::ResidentResult SlotCache::make_resident(uint32_t g, const std::vector
     want[key(g, u)] = 1;
   }
   size_t n_other = 0;
-  for (uint32_t k : other_kept)
-    if (k < keys_ && !other[k] && !want[k]) {
-      other[k] = 1;
-      ++n_other;
-    }
+  for (uint32_t k : other_kept) {
+    if (k >= keys_ || other[k] || want[k]) continue;
+    other[k] = 1;
+    ++n_other;
+  }
   // capacity: every layer's kept units leave the spare target free for the boundaries
-  const uint64_t cap = uint64_t(c_.persistent_slots) - c_.spare_target;
-  require(ids.size() + n_other <= cap, SS_E_CAPACITY,
+  const uint64_t room = uint64_t(c_.persistent_slots) - c_.spare_target;
+  require(ids.size() + n_other <= room, SS_E_CAPACITY,
           "ss_dg_make_resident: " + std::to_string(ids.size()) + " units of gated layer " + std::to_string(g) + " + " +
               std::to_string(n_other) + " other kept units + the spare target " + std::to_string(c_.spare_target) +
               " exceed the " + std::to_string(c_.persistent_slots) + " persistent slots");
-  size_t need = 0, eligible_n = 0, evicting = 0, discarded = 0;
+  size_t to_copy = 0, evictable = 0, evicting = 0;
   for (uint32_t k = 0; k < keys_; ++k) {
-    const Entry& x = e_[k];
-    require(x.home != Home::Bank, SS_E_BACKEND, "ss_dg_make_resident: a bank unit between tokens");
-    if (x.home == Home::Evicting) ++evicting;
-    if (want[k]) need += x.home != Home::Device && x.home != Home::Coming ? 1u : 0u;
-    else if (x.home == Home::Device && !other[k]) ++eligible_n;
+    const Home h = e_[k].home;
+    require(h != Home::Bank, SS_E_BACKEND, "ss_dg_make_resident: a bank unit between tokens");
+    evicting += h == Home::Evicting ? 1 : 0;
+    if (want[k]) to_copy += h != Home::Device && h != Home::Coming ? 1 : 0;
+    else evictable += h == Home::Device && !other[k] ? 1 : 0;
   }
-  for (const Writeback& w : wbs_) discarded += w.discard ? 1u : 0u;
+  const size_t discards = size_t(std::count_if(wbs_.begin(), wbs_.end(), [](const Writeback& w) { return w.discard; }));
   const size_t free_after = free_slots_.size() + evicting;
-  require(need <= free_after + eligible_n, SS_E_CAPACITY,
-          "ss_dg_make_resident: " + std::to_string(need) + " units to copy in, " + std::to_string(free_after) +
-              " free slots and " + std::to_string(eligible_n) +
+  require(to_copy <= free_after + evictable, SS_E_CAPACITY,
+          "ss_dg_make_resident: " + std::to_string(to_copy) + " units to copy in, " + std::to_string(free_after) +
+              " free slots and " + std::to_string(evictable) +
               " evictable units (the rest hold other layers' kept units or prefetches in flight)");
-  require(c_.disk_tier || need <= free_after || free_after + free_blocks_.size() + discarded > 0, SS_E_CAPACITY,
+  require(c_.disk_tier || to_copy <= free_after || free_after + free_blocks_.size() + discards > 0, SS_E_CAPACITY,
           "ss_dg_make_resident: no free slot and no free pinned block to start the write-backs");
   stamp_room("ss_dg_make_resident");
-  drain();  // everything settled: reads, copies, deferred and recorded write-backs collected
-  for (const Writeback& w : wbs_) m_->event_sync(w.done);
-  collect();
-  if (!wbs_.empty()) broken("ss_dg_make_resident: write-backs not collected");
+  settle_writebacks("ss_dg_make_resident");
 
-  ResidentResult r;
+  ResidentResult res;
   std::vector<uint32_t> in;  // the units to copy in, in the caller's order
   for (uint32_t u : ids) {
     const uint32_t k = key(g, u);
     Entry& x = e_[k];
-    if (x.home == Home::Coming) {  // a prefetch whose copy landed: admitted now
-      x.home = Home::Device;
-      x.via_pf = false;
-      if (x.pf_done) {
-        pool_.push_back(x.pf_done);
-        x.pf_done = nullptr;
-      }
-      if (x.block >= 0) {
-        free_blocks_.push_back(x.block);
-        x.block = -1;
-      }
-    } else if (x.home != Home::Device) {
+    if (x.home == Home::Device) continue;
+    if (x.home != Home::Coming) {
       in.push_back(k);
+      continue;
     }
+    x.home = Home::Device;  // a prefetch whose copy landed: admitted now
+    x.via_pf = false;
+    recycle(x.pf_done);
+    if (x.block >= 0) free_blocks_.give(x.block);
+    x.block = -1;
   }
   auto eligible = [&](uint32_t k) {
     const Entry& x = e_[k];
@@ -1272,161 +1174,156 @@ SlotCache::ResidentResult SlotCache::make_resident(uint32_t g, const std::vector
   };
   std::vector<uint32_t> victims;
   const size_t n_vict = in.size() > free_slots_.size() ? in.size() - free_slots_.size() : 0;
-  if (n_vict && c_.scored) {
+  if (n_vict != 0 && c_.scored) {
     select_scored(n_vict, eligible, false);
     for (const ScoreCand& cd : select_heap_) victims.push_back(cd.key);
   } else {
-    for (uint32_t k = tail_; k != kNil && victims.size() < n_vict; k = e_[k].prev)
+    for (uint32_t k = recent_.back(); k != kNil && victims.size() < n_vict; k = recent_.newer(k))
       if (eligible(k)) victims.push_back(k);
   }
   if (victims.size() != n_vict) broken("ss_dg_make_resident: fewer victims than the capacity check counted");
 
   std::vector<uint8_t> hold = want;  // never dropped to a file here: the units to copy in, this call's write-backs
   std::vector<int32_t> released;     // source blocks of committed copies (free once the demand stream synced)
-  std::vector<int32_t> wb;           // slots of written-back victims (free once the write-back stream synced)
+  std::vector<int32_t> written;      // slots of written-back victims (free once the write-back stream synced)
   struct Read {
     uint32_t key;
     int32_t slot, stage;
     void* handle;
   };
   std::deque<Read> reads;  // file reads in flight, oldest first, each in its own staging buffer
-  const size_t depth = c_.disk_tier ? std::max<size_t>(1, std::min<size_t>(std::max<uint32_t>(c_.disk_queue, 1),
-                                                                          c_.disk_staging))
-                                    : 1;
-  bool io_error = false;
-  // the committed units become the most recent in the order of `in` on every exit
-  struct Recent {
-    SlotCache* cache;
+  const size_t depth =
+      c_.disk_tier ? std::max<size_t>(1, std::min<size_t>(std::max<uint32_t>(c_.disk_queue, 1), c_.disk_staging)) : 1;
+  bool io_failed = false;
+  uint64_t n_read = 0, n_written = 0, read_ns = 0;
+  // the committed units become the most recent, in the order of `in`, on every exit
+  std::vector<uint8_t> committed(in.size(), 0);
+  struct Promote {
+    SlotCache& cache;
     const std::vector<uint32_t>& order;
-    std::vector<uint8_t> done;
-    ~Recent() {
+    const std::vector<uint8_t>& done;
+    ~Promote() {
       for (size_t i = 0; i < order.size(); ++i)
-        if (done[i]) cache->push_front(order[i]);
+        if (done[i]) cache.touch(order[i]);
     }
-  } recent{this, in, std::vector<uint8_t>(in.size(), 0)};
-  std::vector<int32_t> in_pos(keys_, -1);
-  for (size_t i = 0; i < in.size(); ++i) in_pos[in[i]] = int32_t(i);
+  } promote{*this, in, committed};
+  std::vector<int32_t> position(keys_, -1);
+  for (size_t i = 0; i < in.size(); ++i) position[in[i]] = int32_t(i);
   auto commit = [&](uint32_t k, int32_t slot) {
     Entry& x = e_[k];
     x.home = Home::Device;
     x.slot = slot;
     x.block = -1;
-    recent.done[size_t(in_pos[k])] = 1;
+    committed[size_t(position[k])] = 1;
     ++on_device_;
-    ++r.copied;
+    ++res.copied;
   };
-  auto transfer = [&](uint32_t k, int32_t slot, int32_t src) {  // the copy and its entry, or nothing owned changes
+  auto copy_in = [&](uint32_t k, int32_t slot, int32_t src) {  // the copy and its entry, or nothing owned changes
     try {
       m_->h2d(Mover::kDem, slot, src, k);
       publish(Mover::kDem, k, slot);
     } catch (...) {
       table_[k] = -1;
-      free_slots_.push_back(slot);
+      free_slots_.give(slot);
       throw;
     }
   };
-  auto flush_dem = [&] {
+  auto settle_copies = [&] {
     m_->sync(Mover::kDem);
-    free_blocks_.insert(free_blocks_.end(), released.begin(), released.end());
+    for (int32_t b : released) free_blocks_.give(b);
     released.clear();
   };
-  auto flush_d2h = [&] {
-    if (wb.empty()) return;
+  auto settle_writes = [&] {
+    if (written.empty()) return;
     m_->sync(Mover::kD2h);
-    free_slots_.insert(free_slots_.end(), wb.begin(), wb.end());
-    wb.clear();
-  };
-  uint64_t n_read = 0, n_wb = 0, read_ns = 0;
-  auto timed = [&](const std::chrono::steady_clock::time_point& a) {
-    read_ns += uint64_t(
-        std::chrono::duration_cast<std::chrono::nanoseconds>(std::chrono::steady_clock::now() - a).count());
+    for (int32_t s : written) free_slots_.give(s);
+    written.clear();
   };
   auto end_read = [&](size_t i) {  // a read's end: its copy and entry, its staging buffer's event
     const Read rd = reads[i];
     reads.erase(reads.begin() + std::ptrdiff_t(i));
-    const auto ta = std::chrono::steady_clock::now();
+    const auto ta = Clock::now();
     try {
       m_->read_end(rd.handle);
     } catch (...) {
-      timed(ta);
-      io_error = true;
-      free_slots_.push_back(rd.slot);
+      read_ns += ns_since(ta);
+      io_failed = true;
+      free_slots_.give(rd.slot);
       throw;
     }
-    timed(ta);
-    transfer(rd.key, rd.slot, rd.stage);
+    read_ns += ns_since(ta);
+    copy_in(rd.key, rd.slot, rd.stage);
     --on_file_;
     commit(rd.key, rd.slot);
     ++n_read;
     void*& ev = stage_ev_[uint32_t(rd.stage) - c_.blocks];
-    if (!ev) ev = event();
+    if (ev == nullptr) ev = event();
     m_->record(ev, Mover::kDem);
   };
   auto account = [&] {
-    st_.resident_units += r.copied;
-    st_.resident_evicted += r.evicted;
-    st_.resident_bytes += uint64_t(r.copied) * unit_bytes_;
+    const uint64_t copied_bytes = uint64_t(res.copied) * unit_bytes_;
+    st_.resident_units += res.copied;
+    st_.resident_evicted += res.evicted;
+    st_.resident_bytes += copied_bytes;
     st_.mkres_file_reads += n_read;
     st_.mkres_file_bytes += n_read * unit_bytes_;
     st_.mkres_read_ns += read_ns;
-    st_.mkres_h2d_bytes += uint64_t(r.copied) * unit_bytes_;
-    st_.mkres_wb_bytes += n_wb * unit_bytes_;
-    st_.resident_ns += uint64_t(
-        std::chrono::duration_cast<std::chrono::nanoseconds>(std::chrono::steady_clock::now() - t0).count());
+    st_.mkres_h2d_bytes += copied_bytes;
+    st_.mkres_wb_bytes += n_written * unit_bytes_;
+    st_.resident_ns += ns_since(t0);
+  };
+  // With no free slot: victims evicted until the free slots and those being written back cover the units left to
+  // copy; no copy for a clean one or one dropped to its file (a pinned unit dropped to its file frees a block when
+  // none is free), else written back into a free block.
+  size_t vi = 0;
+  auto evict_for = [&](size_t left) {
+    while (vi < victims.size() && free_slots_.size() + written.size() < left) {
+      const uint32_t v = victims[vi];
+      Entry& x = e_[v];
+      if (!x.backed && free_blocks_.empty() && !released.empty()) {  // the blocks of the copies already enqueued
+        settle_copies();
+        continue;
+      }
+      if (!x.backed && free_blocks_.empty() && !c_.disk_tier) break;
+      const bool clean = !x.backed && clean_now();
+      const bool no_copy = x.backed || clean || (free_blocks_.empty() && !drop_host_lru(&hold, false));
+      if (clean) count_clean();
+      int32_t b = -1;
+      if (!no_copy) {
+        b = free_blocks_.items().back();
+        m_->d2h(Mover::kD2h, x.slot, b, -1, v);  // the dirty unit's only copy, written back before its slot is reused
+        free_blocks_.take();
+        ++n_written;
+      }
+      ++vi;
+      ++res.evicted;
+      leave_device(v);
+      if (no_copy) {
+        free_slots_.give(x.slot);
+        to_lower(v);
+        continue;
+      }
+      written.push_back(x.slot);
+      x.home = Home::Host;
+      x.slot = -1;
+      x.block = b;
+      home_push(v);
+      hold[v] = 1;
+    }
   };
   try {
-    size_t next = 0, vi = 0;
-    while (next < in.size()) {
-      // no free slot: the next victims (as many as the remaining units need and the blocks allow)
-      const bool evict = free_slots_.empty();
-      while (evict && vi < victims.size() && free_slots_.size() + wb.size() < in.size() - next) {
-        const uint32_t v = victims[vi];
-        Entry& x = e_[v];
-        if (!x.backed && free_blocks_.empty() && !released.empty()) {  // the blocks of the copies already enqueued
-          flush_dem();
-          continue;
-        }
-        if (!x.backed && free_blocks_.empty() && !c_.disk_tier) break;
-        // a clean copy (its block is its home again) or, file tier with no block to free (clean_evict: none
-        // free), its file: no copy
-        const bool clean = !x.backed && clean_now();
-        const bool no_copy = x.backed || clean || (free_blocks_.empty() && !drop_host_lru(&hold, false));
-        if (clean) count_clean();
-        int32_t b = -1;
-        if (!no_copy) {
-          b = free_blocks_.back();
-          m_->d2h(Mover::kD2h, x.slot, b, -1, v);  // the dirty unit's only copy, written back before its slot is reused
-          free_blocks_.pop_back();
-          ++n_wb;
-        }
-        ++vi;
-        ++r.evicted;
-        unlink(v);
-        --on_device_;
-        table_[v] = -1;
-        if (no_copy) {
-          free_slots_.push_back(x.slot);
-          to_lower(v);
-          continue;
-        }
-        wb.push_back(x.slot);
-        x.home = Home::Host;
-        x.slot = -1;
-        x.block = b;
-        hpush(v);
-        hold[v] = 1;
-      }
-      flush_d2h();
+    for (size_t next = 0; next < in.size();) {
+      if (free_slots_.empty()) evict_for(in.size() - next);
+      settle_writes();
       if (free_slots_.empty()) fail(SS_E_BACKEND, "ss_dg_make_resident: no slot for a unit");
-      const int32_t slot = free_slots_.back();
-      free_slots_.pop_back();
+      const int32_t slot = free_slots_.take();
       const uint32_t k = in[next];
       Entry& x = e_[k];
       if (x.home == Home::Host) {
         const int32_t b = x.block;
-        transfer(k, slot, b);
+        copy_in(k, slot, b);
         ++next;
-        hunlink(k);
+        home_erase(k);
         released.push_back(b);
         commit(k, slot);
         continue;
@@ -1441,34 +1338,31 @@ SlotCache::ResidentResult SlotCache::make_resident(uint32_t g, const std::vector
           }
         if (reads.size() >= depth) end_read(0);
         const uint32_t i = stage_next_;
-        stage_next_ = (i + 1) % c_.disk_staging;
+        stage_next_ = (stage_next_ + 1) % c_.disk_staging;
         const int32_t stage = int32_t(c_.blocks + i);
-        for (size_t j = 0; j < reads.size(); ++j)
-          if (reads[j].stage == stage) {
-            end_read(j);
-            break;
-          }
-        if (stage_ev_[i] && !m_->done(stage_ev_[i])) m_->event_sync(stage_ev_[i]);
-        void* h = nullptr;
-        const auto tb = std::chrono::steady_clock::now();
+        const auto holder = std::find_if(reads.begin(), reads.end(), [stage](const Read& r) { return r.stage == stage; });
+        if (holder != reads.end()) end_read(size_t(holder - reads.begin()));
+        if (stage_ev_[i] != nullptr && !m_->done(stage_ev_[i])) m_->event_sync(stage_ev_[i]);
+        const auto tb = Clock::now();
+        void* handle = nullptr;
         try {
-          h = m_->read_begin(k, stage);
+          handle = m_->read_begin(k, stage);
         } catch (...) {
-          timed(tb);
-          io_error = true;
+          read_ns += ns_since(tb);
+          io_failed = true;
           throw;
         }
-        timed(tb);
-        reads.push_back({k, slot, stage, h});
+        read_ns += ns_since(tb);
+        reads.push_back(Read{k, slot, stage, handle});
         ++next;
       } catch (...) {
-        free_slots_.push_back(slot);
+        free_slots_.give(slot);
         throw;
       }
     }
     while (!reads.empty()) end_read(0);
-    flush_d2h();
-    flush_dem();
+    settle_writes();
+    settle_copies();
     m_->upload_table(table_.data(), keys_);  // (syncs the demand stream) every changed entry, the victims' -1 included
   } catch (...) {
     for (const Read& rd : reads) {  // reads not ended give their slots back (their keys never changed home)
@@ -1476,30 +1370,30 @@ SlotCache::ResidentResult SlotCache::make_resident(uint32_t g, const std::vector
         m_->read_end(rd.handle);
       } catch (...) {
       }
-      free_slots_.push_back(rd.slot);
+      free_slots_.give(rd.slot);
     }
     reads.clear();
-    bool ok = false;
-    if (io_error) {  // the device is fine: what was enqueued lands, the table goes up
+    bool uploaded = false;
+    if (io_failed) {  // the device is fine: what was enqueued lands, the table goes up
       try {
-        flush_d2h();
-        flush_dem();
+        settle_writes();
+        settle_copies();
         m_->upload_table(table_.data(), keys_);
-        ok = true;
+        uploaded = true;
       } catch (...) {
       }
     }
-    if (!ok) {  // a device failure: the host records stay one ownership (the context is poisoned by its caller)
-      free_slots_.insert(free_slots_.end(), wb.begin(), wb.end());
-      wb.clear();
-      free_blocks_.insert(free_blocks_.end(), released.begin(), released.end());
+    if (!uploaded) {  // a device failure: the host records stay one ownership (the context is poisoned by its caller)
+      for (int32_t s : written) free_slots_.give(s);
+      for (int32_t b : released) free_blocks_.give(b);
+      written.clear();
       released.clear();
     }
     account();
     throw;
   }
   account();
-  return r;
+  return res;
 }
 
 // ---- placement rounds ----
@@ -1511,11 +1405,11 @@ SlotCache::ResidentResult SlotCache::make_resident(uint32_t g, const std::vector
 // of the coldest pinned unit (dropped to its file) when hotter by the hysteresis factor. A unit with no count never
 // moves; every step checks the budgets and the cancellation first (dg_core.cpp:2592-2897).
 RoundOut SlotCache::round(const RoundIn& in, const std::vector<uint32_t>& kept_keys) {
-  const auto t0 = std::chrono::steady_clock::now();
+  const auto t0 = Clock::now();
   round_state_.store(kRoundRunning, std::memory_order_release);
-  struct Idle {
-    std::atomic<int>& s;
-    ~Idle() { s.store(kRoundIdle, std::memory_order_release); }
+  struct BackToIdle {
+    std::atomic<int>& state;
+    ~BackToIdle() { state.store(kRoundIdle, std::memory_order_release); }
   } idle{round_state_};
   last_round_ = RoundOut{};
   require(std::isfinite(in.decay) && in.decay >= 0 && in.decay <= 1, SS_E_INVALID, "ss_dg_round: decay must be 0..1");
@@ -1524,243 +1418,225 @@ RoundOut SlotCache::round(const RoundIn& in, const std::vector<uint32_t>& kept_k
   require(in.flags == 0, SS_E_INVALID, "ss_dg_round: unknown flags");
   std::vector<uint8_t> kept(keys_, 0);
   size_t n_kept = 0;
-  for (uint32_t k : kept_keys)
-    if (k < keys_ && !kept[k]) {
-      kept[k] = 1;
-      ++n_kept;
-    }
-  for (uint32_t k = 0; k < keys_; ++k)
-    if (e_[k].home == Home::Bank) broken("a bank unit between tokens");
+  for (uint32_t k : kept_keys) {
+    if (k >= keys_ || kept[k]) continue;
+    kept[k] = 1;
+    ++n_kept;
+  }
+  if (std::any_of(e_.begin(), e_.end(), [](const Entry& x) { return x.home == Home::Bank; }))
+    broken("a bank unit between tokens");
   stamp_room("ss_dg_round");
-  drain();  // everything settled: copies, deferred and recorded write-backs collected
-  for (const Writeback& w : wbs_) m_->event_sync(w.done);
-  collect();
-  if (!wbs_.empty()) broken("ss_dg_round: write-backs not collected");
+  settle_writebacks("ss_dg_round");
   for (uint32_t k = 0; k < keys_; ++k) {
     rs_[k] = in.decay * rs_[k] + double(rhits_[k]);
     rhits_[k] = 0;
   }
 
-  RoundOut r;
+  RoundOut out;
   const uint64_t ub = unit_bytes_;
   uint64_t spent = 0;
   uint32_t moved = 0;
-  auto fits = [&](uint64_t b) { return !in.budget_bytes || (spent <= in.budget_bytes && b <= in.budget_bytes - spent); };
-  auto cancelled = [&] {
-    if (round_state_.load(std::memory_order_acquire) == kRoundCancel) r.cancelled = 1;
-    return r.cancelled != 0;
+  auto affordable = [&](uint64_t b) {
+    return in.budget_bytes == 0 || (spent <= in.budget_bytes && b <= in.budget_bytes - spent);
   };
-  std::vector<uint32_t> pos(keys_, 0), hpos(keys_, 0);  // recency positions, least recent first
-  {
-    uint32_t i = 0;
-    for (uint32_t k = tail_; k != kNil; k = e_[k].prev) pos[k] = i++;
-  }
+  auto stop_asked = [&] {
+    if (round_state_.load(std::memory_order_acquire) == kRoundCancel) out.cancelled = 1;
+    return out.cancelled != 0;
+  };
+  // recency positions, least recent first (device homes; pinned homes filled before (b))
+  std::vector<uint32_t> age(keys_, 0), home_age(keys_, 0);
+  uint32_t next_age = 0;
+  for (uint32_t k = recent_.back(); k != kNil; k = recent_.newer(k)) age[k] = next_age++;
   auto hotter = [&](uint32_t a, uint32_t b) { return rs_[a] != rs_[b] ? rs_[a] > rs_[b] : a < b; };
-  auto colder_dev = [&](uint32_t a, uint32_t b) {
-    if (rs_[a] != rs_[b]) return rs_[a] < rs_[b];
-    return pos[a] != pos[b] ? pos[a] < pos[b] : a < b;
-  };
-  auto colder_host = [&](uint32_t a, uint32_t b) {
-    if (rs_[a] != rs_[b]) return rs_[a] < rs_[b];
-    return hpos[a] != hpos[b] ? hpos[a] < hpos[b] : a < b;
+  auto colder = [&](const std::vector<uint32_t>& rank) {
+    return [&](uint32_t a, uint32_t b) {
+      if (rs_[a] != rs_[b]) return rs_[a] < rs_[b];
+      return rank[a] != rank[b] ? rank[a] < rank[b] : a < b;
+    };
   };
   std::vector<uint32_t> dev, host, file;
   size_t n_coming = 0;
   for (uint32_t k = 0; k < keys_; ++k) {
     const Entry& x = e_[k];
-    if (x.home == Home::Coming) ++n_coming;
+    n_coming += x.home == Home::Coming ? 1 : 0;
     if (kept[k] || x.wb_pending) continue;
     if (x.home == Home::Device) dev.push_back(k);
     else if (x.home == Home::Host) host.push_back(k);
     else if (x.home == Home::File) file.push_back(k);
   }
-  std::sort(dev.begin(), dev.end(), colder_dev);
+  std::sort(dev.begin(), dev.end(), colder(age));
   std::sort(host.begin(), host.end(), hotter);
   std::sort(file.begin(), file.end(), hotter);
-  int64_t room = int64_t(c_.persistent_slots) - int64_t(c_.spare_target) - int64_t(n_kept) - int64_t(n_coming) -
-                 int64_t(dev.size());
-  const Mover::Stream ws = c_.wb_on_d2h ? Mover::kD2h : Mover::kDem;
+  int64_t share = int64_t(c_.persistent_slots) - int64_t(c_.spare_target) - int64_t(n_kept) - int64_t(n_coming) -
+                  int64_t(dev.size());
+  const Mover::Stream wb_stream = c_.wb_on_d2h ? Mover::kD2h : Mover::kDem;
   auto account = [&] {
-    r.ns = uint64_t(
-        std::chrono::duration_cast<std::chrono::nanoseconds>(std::chrono::steady_clock::now() - t0).count());
+    out.ns = ns_since(t0);
     ++st_.round_count;
-    st_.round_units += uint64_t(r.promoted_to_device) + r.promoted_to_pinned + r.demoted_from_device + r.dropped_to_file;
-    st_.round_bytes += r.bytes_read + r.bytes_h2d + r.bytes_written_back;
-    st_.round_ns += r.ns;
-    st_.round_cancelled += r.cancelled;
-    last_round_ = r;
+    st_.round_units += uint64_t(out.promoted_to_device) + out.promoted_to_pinned + out.demoted_from_device +
+                       out.dropped_to_file;
+    st_.round_bytes += out.bytes_read + out.bytes_h2d + out.bytes_written_back;
+    st_.round_ns += out.ns;
+    st_.round_cancelled += out.cancelled;
+    last_round_ = out;
   };
   // a pinned unit into `slot`: its home changes once the copy and its entry were accepted and the demand stream synced;
   // a cancellation seen then drops it (the slot free again, the unit keeps its block)
   auto promote = [&](uint32_t k, int32_t slot) {
     Entry& x = e_[k];
-    const int32_t b = x.block;
+    const int32_t src = x.block;
     try {
-      m_->h2d(Mover::kDem, slot, b, k);
+      m_->h2d(Mover::kDem, slot, src, k);
       publish(Mover::kDem, k, slot);
       m_->sync(Mover::kDem);
     } catch (...) {
       table_[k] = -1;
-      free_slots_.push_back(slot);
+      free_slots_.give(slot);
       throw;
     }
     spent += ub;
-    r.bytes_h2d += ub;
-    if (cancelled()) {
+    out.bytes_h2d += ub;
+    if (stop_asked()) {
       table_[k] = -1;
-      free_slots_.push_back(slot);
+      free_slots_.give(slot);
       return false;
     }
-    hunlink(k);
-    free_blocks_.push_back(b);
+    home_erase(k);
+    free_blocks_.give(src);
     x.block = -1;
     x.slot = slot;
     x.home = Home::Device;
-    push_front(k);
+    touch(k);
     ++on_device_;
-    ++r.promoted_to_device;
+    ++out.promoted_to_device;
     return true;
+  };
+  // a pinned unit dropped to its file (no copy: the file holds its bytes); its block is returned
+  auto drop_to_file = [&](uint32_t p) {
+    Entry& y = e_[p];
+    home_erase(p);
+    const int32_t b = y.block;
+    y.block = -1;
+    y.home = Home::File;
+    ++on_file_;
+    ++out.dropped_to_file;
+    return b;
   };
   // a block for a demoted unit's write-back: a free one, else (file tier) the coldest pinned unit's, dropped to its
   // file (never `except`); -1 when none
-  size_t hback = host.size();
-  auto wb_block = [&](uint32_t except) -> int32_t {
-    if (!free_blocks_.empty()) {
-      const int32_t b = free_blocks_.back();
-      free_blocks_.pop_back();
-      return b;
-    }
+  size_t coldest = host.size();
+  auto block_for_writeback = [&](uint32_t except) -> int32_t {
+    if (!free_blocks_.empty()) return free_blocks_.take();
     if (!c_.disk_tier) return -1;
-    while (hback > 0) {
-      const uint32_t p = host[--hback];
-      Entry& y = e_[p];
-      if (p == except || y.home != Home::Host) continue;
-      hunlink(p);
-      const int32_t b = y.block;
-      y.block = -1;
-      y.home = Home::File;
-      ++on_file_;
-      ++r.dropped_to_file;
-      return b;
+    while (coldest > 0) {
+      const uint32_t p = host[--coldest];
+      if (p != except && e_[p].home == Home::Host) return drop_to_file(p);
     }
     return -1;
   };
   // (b)'s reads: one at a time (synchronous), each committed at the next read or at the end
-  struct Rd {
+  struct Landing {
     uint32_t key;
     int32_t block;
   };
-  std::deque<Rd> reads;
-  auto end_read = [&] {
-    const Rd rd = reads.front();
+  std::deque<Landing> reads;
+  auto commit_read = [&] {
+    const Landing rd = reads.front();
     reads.pop_front();
-    r.bytes_read += ub;
-    if (cancelled()) {  // the block free again, the unit stays in its file
-      free_blocks_.push_back(rd.block);
+    out.bytes_read += ub;
+    if (stop_asked()) {  // the block free again, the unit stays in its file
+      free_blocks_.give(rd.block);
       return;
     }
     Entry& x = e_[rd.key];
     --on_file_;
     x.home = Home::Host;
     x.block = rd.block;
-    hpush(rd.key);
-    ++r.promoted_to_pinned;
+    home_push(rd.key);
+    ++out.promoted_to_pinned;
   };
   try {
-    size_t j = 0;
+    size_t next_dev = 0;
     for (size_t i = 0; i < host.size() && moved < in.max_units; ++i) {  // (a) pinned -> device
       const uint32_t c = host[i];
       if (!(rs_[c] > 0)) break;
       if (e_[c].home != Home::Host) continue;  // (dropped to its file for a write-back block)
-      if (cancelled()) break;
-      if (room > 0 && free_slots_.size() > c_.spare_target) {  // the device holds less than its share
-        if (!fits(ub)) break;
-        const int32_t slot = free_slots_.back();
-        free_slots_.pop_back();
-        if (!promote(c, slot)) break;
-        --room;
+      if (stop_asked()) break;
+      if (share > 0 && free_slots_.size() > c_.spare_target) {  // the device holds less than its share
+        if (!affordable(ub)) break;
+        if (!promote(c, free_slots_.take())) break;
+        --share;
         ++moved;
         continue;
       }
-      if (j >= dev.size()) break;
-      const uint32_t v = dev[j];
+      if (next_dev >= dev.size()) break;
+      const uint32_t v = dev[next_dev];
       if (!(rs_[c] > in.hysteresis * rs_[v])) break;
       Entry& y = e_[v];
       const bool clean = !y.backed && clean_now();  // clean_evict: no free block, to its file (no write)
-      if (!fits(ub + (y.backed || clean ? 0 : ub))) break;
+      const bool free_demotion = y.backed || clean;
+      if (!affordable(ub + (free_demotion ? 0 : ub))) break;
       const int32_t slot = y.slot;
-      if (y.backed || clean) {  // a clean copy: its block is its home again, no write (clean_evict: its file)
-        unlink(v);
-        --on_device_;
-        table_[v] = -1;
+      if (free_demotion) {  // a clean copy: its block is its home again, no write (clean_evict: its file)
+        leave_device(v);
         to_lower(v);
         if (clean) count_clean();
       } else {
-        const int32_t b = wb_block(c);
+        const int32_t b = block_for_writeback(c);
         if (b < 0) break;
         try {
-          m_->d2h(ws, slot, b, -1, v);
-          m_->sync(ws);
+          m_->d2h(wb_stream, slot, b, -1, v);
+          m_->sync(wb_stream);
         } catch (...) {
-          free_blocks_.push_back(b);  // the unit keeps its slot (its only copy)
+          free_blocks_.give(b);  // the unit keeps its slot (its only copy)
           throw;
         }
-        unlink(v);
-        --on_device_;
-        table_[v] = -1;
+        leave_device(v);
         y.home = Home::Host;
         y.slot = -1;
         y.block = b;
-        hpush(v);
+        home_push(v);
         spent += ub;
-        r.bytes_written_back += ub;
+        out.bytes_written_back += ub;
       }
-      ++j;
-      ++r.demoted_from_device;
+      ++next_dev;
+      ++out.demoted_from_device;
       if (!promote(c, slot)) break;  // (cancelled: the demoted unit's slot stays free)
       ++moved;
     }
-    if (c_.disk_tier && !r.cancelled) {  // (b) file -> pinned, in place of the coldest pinned units
+    if (c_.disk_tier && !out.cancelled) {  // (b) file -> pinned, in place of the coldest pinned units
       std::vector<uint32_t> pinned;
       for (uint32_t k = 0; k < keys_; ++k)
         if (e_[k].home == Home::Host && !kept[k] && !e_[k].wb_pending) pinned.push_back(k);
-      uint32_t hi = 0;
-      for (uint32_t k = htail_; k != kNil; k = e_[k].hprev) hpos[k] = hi++;  // after (a)'s pushes
-      std::sort(pinned.begin(), pinned.end(), colder_host);
+      uint32_t h_age = 0;
+      for (uint32_t k = homes_.back(); k != kNil; k = homes_.newer(k)) home_age[k] = h_age++;  // after (a)'s pushes
+      std::sort(pinned.begin(), pinned.end(), colder(home_age));
       size_t pv = 0;
       for (size_t i = 0; i < file.size() && moved < in.max_units && pv < pinned.size(); ++i) {
         const uint32_t c = file[i];
         if (!(rs_[c] > 0)) break;
         if (e_[c].home != Home::File) continue;
-        if (cancelled()) break;
-        const uint32_t p = pinned[pv];
-        if (!(rs_[c] > in.hysteresis * rs_[p])) break;
-        if (!fits(ub)) break;
-        if (!reads.empty()) end_read();
-        if (r.cancelled) break;
-        ++pv;
-        Entry& y = e_[p];  // dropped to its file (no copy): its block is quiescent
-        hunlink(p);
-        const int32_t b = y.block;
-        y.block = -1;
-        y.home = Home::File;
-        ++on_file_;
-        ++r.dropped_to_file;
+        if (stop_asked()) break;
+        if (!(rs_[c] > in.hysteresis * rs_[pinned[pv]])) break;
+        if (!affordable(ub)) break;
+        if (!reads.empty()) commit_read();
+        if (out.cancelled) break;
+        const int32_t b = drop_to_file(pinned[pv++]);  // its block is quiescent
         try {
           m_->read_unit(c, b);
         } catch (...) {
-          free_blocks_.push_back(b);
+          free_blocks_.give(b);
           throw;
         }
-        reads.push_back({c, b});
+        reads.push_back(Landing{c, b});
         spent += ub;
         ++moved;
       }
-      while (!reads.empty()) end_read();
+      while (!reads.empty()) commit_read();
     }
     m_->upload_table(table_.data(), keys_);  // (syncs the demand stream) every changed entry
   } catch (...) {
-    for (const Rd& rd : reads) free_blocks_.push_back(rd.block);  // never committed: their units stay in their files
+    for (const Landing& rd : reads) free_blocks_.give(rd.block);  // never committed: their units stay in their files
     reads.clear();
     try {  // the moves made so far go up (a failed device fails this too; the caller then poisons the context)
       m_->upload_table(table_.data(), keys_);
@@ -1770,7 +1646,7 @@ RoundOut SlotCache::round(const RoundIn& in, const std::vector<uint32_t>& kept_k
     throw;
   }
   account();
-  return r;
+  return out;
 }
 
 void SlotCache::seed_round_counts(const std::vector<uint32_t>& keys, const std::vector<float>& counts) {
@@ -1783,45 +1659,43 @@ void SlotCache::seed_round_counts(const std::vector<uint32_t>& keys, const std::
   for (size_t i = 0; i < keys.size(); ++i) rs_[keys[i]] = double(counts[i]);
 }
 
+// Between tokens: pinned units into free slots above the spare target, each copied and made the most recent.
 uint32_t SlotCache::seed(const std::vector<uint32_t>& keys) {
   drain_pending();  // between tokens (copies, then an upload)
   stamp_room("ss_seed");
   if (!coming_.empty()) m_->sync(Mover::kPf);
   collect();
-  uint32_t n = 0;
+  uint32_t seeded = 0;
   for (uint32_t k : keys) {
     require(k < keys_, SS_E_INVALID, "ss_seed: unit out of range");
     Entry& x = e_[k];
     if (x.home != Home::Host || free_slots_.size() <= c_.spare_target) continue;
-    const int32_t slot = free_slots_.back();
-    free_slots_.pop_back();
+    const int32_t slot = free_slots_.take();
     m_->h2d(Mover::kDem, slot, x.block, k);
-    hunlink(k);
-    free_blocks_.push_back(x.block);
+    home_erase(k);
+    free_blocks_.give(x.block);
     x.block = -1;
     x.slot = slot;
     x.home = Home::Device;
     table_[k] = slot;
-    push_front(k);
+    touch(k);
     ++on_device_;
-    ++n;
+    ++seeded;
   }
-  if (n) m_->upload_table(table_.data(), keys_);  // syncs kDem: the copies landed before their blocks are reused
-  return n;
+  if (seeded) m_->upload_table(table_.data(), keys_);  // syncs kDem: the copies landed before their blocks are reused
+  return seeded;
 }
 
 void SlotCache::drain() {
   drain_pending();
   while (!deferred_.empty()) finish_front();
-  m_->sync(Mover::kDem);
-  m_->sync(Mover::kPf);
-  m_->sync(Mover::kD2h);
+  for (Mover::Stream s : {Mover::kDem, Mover::kPf, Mover::kD2h}) m_->sync(s);
 }
 
 std::vector<uint32_t> SlotCache::residency() const {
   std::vector<uint32_t> out;
   out.reserve(on_device_);
-  for (uint32_t k = head_; k != kNil; k = e_[k].next)
+  for (uint32_t k = recent_.front(); k != kNil; k = recent_.older(k))
     if (e_[k].home == Home::Device) out.push_back(k);
   return out;
 }
@@ -1829,8 +1703,7 @@ std::vector<uint32_t> SlotCache::residency() const {
 void SlotCache::set_wb_defer(bool on) {
   drain_pending();  // (settings: between tokens, every read ended first)
   if (on == c_.wb_defer) return;
-  if (!on)
-    while (!deferred_.empty()) finish_front();
+  while (!on && !deferred_.empty()) finish_front();
   c_.wb_defer = on;
   apply_wb_defer();
   credit_ = 0;
@@ -1848,6 +1721,7 @@ void SlotCache::set_clean_evict(bool on) {
   drain_pending();
   c_.clean_evict = on;
 }
+
 void SlotCache::set_pf_revert(bool on) {
   drain_pending();
   c_.pf_revert = on;
@@ -1866,28 +1740,26 @@ void SlotCache::set_pressure(uint32_t free_per_token, uint32_t evict_recent) {
   pressure_recent_ = evict_recent;
 }
 
+// ---- reset to the open placement ----
 // Locations: slots [0, P), blocks [P, P + blocks), the reset staging buffer and (file tier) the unit's file. Every
 // misplaced unit moves once: units going back to their file first (no copy, their location vacated), then chains
 // that end in a free location (each move fills the hole the previous one left; a unit read from its file ends its
 // chain), then the remaining cycles through the staging buffer (dg_core.cpp:2976-3075). The mover executes each move
-// before the next one reads its destination.
+// before the next one reads its destination; consecutive slot-to-slot moves share launches, a move's wave one after
+// every earlier move that reads its destination or writes its source.
 void SlotCache::reset_open() {
-  require(open_e_.size() == keys_, SS_E_INVALID, "device-gated: reset before place");
-  drain();
-  for (const Writeback& w : wbs_) m_->event_sync(w.done);
-  collect();
-  if (!wbs_.empty()) broken("reset could not collect every write-back");
+  require(open_.ent.size() == keys_, SS_E_INVALID, "device-gated: reset before place");
+  settle_writebacks("reset");
   for (Entry& x : e_)
     if (x.pf_done) {
       m_->event_sync(x.pf_done);
-      pool_.push_back(x.pf_done);
-      x.pf_done = nullptr;
+      recycle(x.pf_done);
     }
   for (void* ev : stage_ev_)  // every staging copy landed
     if (ev) m_->event_sync(ev);
-  const size_t P = c_.persistent_slots, N = P + c_.blocks, stage = N, file = N + 1;
-  std::vector<size_t> cur(keys_), dst(keys_);
-  std::vector<uint32_t> occupant(N + 1, kNil), wanted(N + 1, kNil);
+  const size_t P = c_.persistent_slots, N = P + c_.blocks, kStage = N, kFile = N + 1;
+  std::vector<size_t> at(keys_), goal(keys_);
+  std::vector<uint32_t> holder(N + 1, kNil), wants(N + 1, kNil);  // per location: its unit now, the unit it should hold
   for (uint32_t k = 0; k < keys_; ++k) {
     const Entry& x = e_[k];
     if (x.home == Home::Evicting) broken("reset left an evicting unit");
@@ -1895,116 +1767,113 @@ void SlotCache::reset_open() {
     // location, so a bank unit read from its file goes back to it
     const bool on_slot = x.home == Home::Device || (x.home == Home::Coming && x.block < 0);
     const bool in_file = x.home == Home::File || (x.home == Home::Bank && x.block < 0);
-    cur[k] = in_file ? file : on_slot ? size_t(x.slot) : P + size_t(x.block);
-    const Entry& o = open_e_[k];
-    dst[k] = o.home == Home::File ? file : o.home == Home::Device ? size_t(o.slot) : P + size_t(o.block);
-    if (cur[k] != file) occupant[cur[k]] = k;
-    if (dst[k] != file) wanted[dst[k]] = k;
+    at[k] = in_file ? kFile : on_slot ? size_t(x.slot) : P + size_t(x.block);
+    const Entry& o = open_.ent[k];
+    goal[k] = o.home == Home::File ? kFile : o.home == Home::Device ? size_t(o.slot) : P + size_t(o.block);
+    if (at[k] != kFile) holder[at[k]] = k;
+    if (goal[k] != kFile) wants[goal[k]] = k;
   }
   for (uint32_t k = 0; k < keys_; ++k)  // back to its file: its location is vacated, no copy
-    if (dst[k] == file && cur[k] != file) {
-      occupant[cur[k]] = kNil;
-      cur[k] = file;
+    if (goal[k] == kFile && at[k] != kFile) {
+      holder[at[k]] = kNil;
+      at[k] = kFile;
     }
-  // plan every move first (bookkeeping only), then execute them in order; consecutive slot-to-slot moves share
-  // launches: a move's wave is one after every earlier move that reads its destination or writes its source
   struct Move {
     size_t from, to;
     uint32_t key;
   };
-  std::vector<Move> plan;
-  auto move = [&](uint32_t k, size_t to) {
-    const size_t from = cur[k];
-    if (to > N || occupant[to] != kNil) broken("reset would overwrite a live source");
-    plan.push_back({from, to, k});
-    if (from != file) occupant[from] = kNil;
-    occupant[to] = k;
-    cur[k] = to;
+  std::vector<Move> moves;  // planned first (bookkeeping only), executed after
+  auto plan = [&](uint32_t k, size_t to) {
+    const size_t from = at[k];
+    if (to > N || holder[to] != kNil) broken("reset would overwrite a live source");
+    moves.push_back(Move{from, to, k});
+    if (from != kFile) holder[from] = kNil;
+    holder[to] = k;
+    at[k] = to;
   };
-  for (size_t loc = 0; loc < N; ++loc) {
-    size_t hole = loc;
-    while (hole < N && occupant[hole] == kNil && wanted[hole] != kNil) {
-      const uint32_t k = wanted[hole];
-      const size_t next = cur[k];
-      move(k, hole);
-      hole = next;
+  for (size_t loc = 0; loc < N; ++loc)  // chains ending in a free location
+    for (size_t hole = loc; hole < N && holder[hole] == kNil && wants[hole] != kNil;) {
+      const uint32_t k = wants[hole];
+      const size_t vacated = at[k];
+      plan(k, hole);
+      hole = vacated;
     }
-  }
-  for (uint32_t k = 0; k < keys_; ++k) {
-    if (cur[k] == dst[k]) continue;
-    if (cur[k] == file) broken("reset left a file read behind");
-    size_t hole = cur[k];
-    move(k, stage);
-    while (hole != dst[k]) {
-      const uint32_t next = wanted[hole];
+  for (uint32_t k = 0; k < keys_; ++k) {  // cycles, through the staging buffer
+    if (at[k] == goal[k]) continue;
+    if (at[k] == kFile) broken("reset left a file read behind");
+    size_t hole = at[k];
+    plan(k, kStage);
+    while (hole != goal[k]) {
+      const uint32_t next = wants[hole];
       if (next == kNil) broken("reset cycle without a predecessor");
-      const size_t from = cur[next];
-      move(next, hole);
-      hole = from;
+      const size_t vacated = at[next];
+      plan(next, hole);
+      hole = vacated;
     }
-    move(k, hole);
+    plan(k, hole);
   }
-  auto blk = [&](size_t loc) { return loc == stage ? -1 : int32_t(loc - P); };
-  std::vector<std::pair<int32_t, int32_t>> d2d;
-  std::vector<uint32_t> wave;
-  auto flush_d2d = [&] {
-    if (d2d.empty()) return;
-    m_->d2d_moves(d2d, wave);
-    d2d.clear();
-    wave.clear();
+  auto block_at = [&](size_t loc) { return loc == kStage ? -1 : int32_t(loc - P); };
+  std::vector<std::pair<int32_t, int32_t>> slot_moves;
+  std::vector<uint32_t> waves;
+  auto run_slot_moves = [&] {
+    if (slot_moves.empty()) return;
+    m_->d2d_moves(slot_moves, waves);
+    slot_moves.clear();
+    waves.clear();
   };
-  for (const Move& mv : plan) {
+  for (const Move& mv : moves) {
     ++st_.reset_moves;
     st_.reset_bytes += unit_bytes_;
     if (mv.from < P && mv.to < P) {
-      uint32_t w = 0;
-      for (size_t i = 0; i < d2d.size(); ++i)
-        if (size_t(d2d[i].first) == mv.to || size_t(d2d[i].second) == mv.from) w = std::max(w, wave[i] + 1);
-      d2d.push_back({int32_t(mv.from), int32_t(mv.to)});
-      wave.push_back(w);
+      uint32_t wave = 0;
+      for (size_t i = 0; i < slot_moves.size(); ++i)
+        if (size_t(slot_moves[i].first) == mv.to || size_t(slot_moves[i].second) == mv.from)
+          wave = std::max(wave, waves[i] + 1);
+      slot_moves.push_back({int32_t(mv.from), int32_t(mv.to)});
+      waves.push_back(wave);
       continue;
     }
-    flush_d2d();
-    if (mv.from == file && mv.to < P) {  // read into the reset staging buffer, then to the slot
+    run_slot_moves();
+    if (mv.from == kFile && mv.to < P) {  // read into the reset staging buffer, then to the slot
       m_->read_unit(mv.key, -1);
       m_->h2d(Mover::kDem, int32_t(mv.to), -1, mv.key);
       m_->sync(Mover::kDem);
-    } else if (mv.from == file) {
-      m_->read_unit(mv.key, blk(mv.to));
+    } else if (mv.from == kFile) {
+      m_->read_unit(mv.key, block_at(mv.to));
     } else if (mv.from < P) {
-      m_->d2h(Mover::kD2h, int32_t(mv.from), blk(mv.to), -1, mv.key);
+      m_->d2h(Mover::kD2h, int32_t(mv.from), block_at(mv.to), -1, mv.key);
       m_->sync(Mover::kD2h);
     } else if (mv.to < P) {
-      m_->h2d(Mover::kDem, int32_t(mv.to), blk(mv.from), mv.key);
+      m_->h2d(Mover::kDem, int32_t(mv.to), block_at(mv.from), mv.key);
       m_->sync(Mover::kDem);
     } else {
-      m_->h2h(blk(mv.from), blk(mv.to), mv.key);
+      m_->h2h(block_at(mv.from), block_at(mv.to), mv.key);
     }
   }
-  flush_d2d();
-  c_ = open_c_;
+  run_slot_moves();
+  // every host record back to the open's
+  c_ = open_.cfg;
   apply_wb_defer();
-  std::copy(open_e_.begin(), open_e_.end(), e_.begin());
+  e_ = open_.ent;
   reset_score();  // the history's open state (a profile's counts, or none)
   std::fill(rs_.begin(), rs_.end(), 0.0);  // placement rounds: the counts start over
   std::fill(rhits_.begin(), rhits_.end(), 0u);
   backed_ = 0;  // clean copies are dropped: the open holds none
-  std::copy(open_table_.begin(), open_table_.end(), table_.begin());
-  free_slots_ = open_free_slots_;
-  free_blocks_ = open_free_blocks_;
-  head_ = open_head_;
-  tail_ = open_tail_;
-  on_device_ = open_on_device_;
-  hhead_ = open_hhead_;
-  htail_ = open_htail_;
-  on_file_ = open_on_file_;
+  table_ = open_.table;
+  free_slots_ = open_.slots;
+  free_blocks_ = open_.blocks;
+  recent_ = open_.recent;
+  homes_ = open_.homes;
+  on_device_ = open_.on_device;
+  on_file_ = open_.on_file;
   stage_next_ = 0;
   coming_.clear();
   banked_.clear();
   std::fill(bank_key_.begin(), bank_key_.end(), kNil);
-  bank_seq_[0] = bank_seq_[1] = 0;
-  bank_layer_[0] = bank_layer_[1] = kNil;
-  bank_next_[0] = bank_next_[1] = 0;
+  for (int b = 0; b < 2; ++b) {
+    bank_seq_[b] = bank_next_[b] = 0;
+    bank_layer_[b] = kNil;
+  }
   std::fill(pf_layer_.begin(), pf_layer_.end(), 0u);
   pf_token_ = 0;
   pred_.clear();
@@ -2018,75 +1887,78 @@ void SlotCache::reset_open() {
   m_->upload_table(table_.data(), keys_);
 }
 
+// ---- invariants ----
 void SlotCache::check() const {
-  std::vector<uint8_t> slot_used(slots_, 0), block_used(c_.blocks, 0);
-  auto take = [&](std::vector<uint8_t>& v, int64_t i, const char* what) {
+  std::vector<uint8_t> slot_owner(slots_, 0), block_owner(c_.blocks, 0);
+  auto own = [this](std::vector<uint8_t>& v, int64_t i, const char* what) {
     if (i < 0 || size_t(i) >= v.size() || v[size_t(i)]) broken(what);
     v[size_t(i)] = 1;
   };
-  uint32_t listed = 0, dev = 0, hlisted = 0, hosts = 0, files = 0;
-  for (uint32_t k = head_; k != kNil; k = e_[k].next) {
+  uint32_t listed = 0, homes_listed = 0, dev = 0, hosts = 0, files = 0;
+  for (uint32_t k = recent_.front(); k != kNil; k = recent_.older(k)) {
     if (++listed > keys_) broken("the recency list has a cycle");
-    const Home h = e_[k].home;
-    if (h != Home::Device && h != Home::Coming) broken("a listed unit is not on the device");
+    if (e_[k].home != Home::Device && e_[k].home != Home::Coming) broken("a listed unit is not on the device");
   }
-  for (uint32_t k = hhead_; k != kNil; k = e_[k].hnext) {
-    if (++hlisted > keys_) broken("the pinned recency list has a cycle");
-    if (e_[k].home != Home::Host || !e_[k].in_hlist) broken("a unit in the pinned recency list is not a pinned home");
+  for (uint32_t k = homes_.front(); k != kNil; k = homes_.older(k)) {
+    if (++homes_listed > keys_) broken("the pinned recency list has a cycle");
+    if (e_[k].home != Home::Host) broken("a unit in the pinned recency list is not a pinned home");
   }
   for (uint32_t k = 0; k < keys_; ++k) {
     const Entry& x = e_[k];
+    const bool in_recent = recent_.has(k);
     switch (x.home) {
       case Home::Host:
-        take(block_used, x.block, "a host unit without its own block");
+        own(block_owner, x.block, "a host unit without its own block");
         if (table_[k] != -1) broken("a host unit with a published entry");
-        if (x.listed) broken("a host unit in the recency list");
+        if (in_recent) broken("a host unit in the recency list");
         ++hosts;
         break;
       case Home::File:
         if (!c_.disk_tier) broken("a file home without the file tier");
-        if (x.slot >= 0 || x.block >= 0 || x.listed || x.in_hlist) broken("a file home holding a slot or a block");
+        if (x.slot >= 0 || x.block >= 0 || in_recent || homes_.has(k)) broken("a file home holding a slot or a block");
         if (table_[k] != -1) broken("a file home with a published entry");
         ++files;
         break;
       case Home::Device:
       case Home::Coming:
         ++dev;
-        take(slot_used, x.slot, "a device unit without its own slot");
+        own(slot_owner, x.slot, "a device unit without its own slot");
         if (x.slot >= int32_t(c_.persistent_slots)) broken("a device unit in a bank slot");
         if (table_[k] != x.slot) broken("a device unit's entry is not its slot");
-        if (!x.listed) broken("a device unit outside the recency list");
-        if (x.home == Home::Coming && (x.block >= 0 || !c_.disk_tier))
-          take(block_used, x.block, "a coming unit without its source block");
-        else if (x.home == Home::Coming) {  // (read from its file)
-        } else if (x.backed) take(block_used, x.block, "a clean copy without its own block");
-        else if (x.block >= 0) broken("a device unit still holding a block");
+        if (!in_recent) broken("a device unit outside the recency list");
+        if (x.home == Home::Coming) {
+          if (x.block >= 0 || !c_.disk_tier) own(block_owner, x.block, "a coming unit without its source block");
+        } else if (x.backed) {
+          own(block_owner, x.block, "a clean copy without its own block");
+        } else if (x.block >= 0) {
+          broken("a device unit still holding a block");
+        }
         if (x.backed && x.home != Home::Device) broken("a clean copy of a unit not on the device");
         break;
       case Home::Bank:
-        take(slot_used, x.slot, "a bank unit without its own slot");
-        if (x.block >= 0 || !c_.disk_tier) take(block_used, x.block, "a bank unit without its block");
+        own(slot_owner, x.slot, "a bank unit without its own slot");
+        if (x.block >= 0 || !c_.disk_tier) own(block_owner, x.block, "a bank unit without its block");
         if (x.slot < int32_t(c_.persistent_slots)) broken("a bank unit in a persistent slot");
         if (table_[k] != x.slot) broken("a bank unit's entry is not its slot");
         break;
       case Home::Evicting:
-        take(slot_used, x.slot, "an evicting unit without its slot");
-        take(block_used, x.block, "an evicting unit without its destination block");
+        own(slot_owner, x.slot, "an evicting unit without its slot");
+        own(block_owner, x.block, "an evicting unit without its destination block");
         if (table_[k] != -1) broken("an evicting unit with a published entry");
         break;
     }
   }
   if (dev != on_device_ || dev != listed) broken("the device count disagrees with the homes");
   if (files != on_file_) broken("the file count disagrees with the homes");
-  if (c_.disk_tier && hosts != hlisted) broken("the pinned recency list does not hold every pinned home");
-  for (int32_t s : free_slots_) take(slot_used, s, "a free slot that is also in use");
-  for (int32_t b : free_blocks_) take(block_used, b, "a free block that is also in use");
+  if (c_.disk_tier && hosts != homes_listed) broken("the pinned recency list does not hold every pinned home");
+  for (int32_t s : free_slots_.items()) own(slot_owner, s, "a free slot that is also in use");
+  for (int32_t b : free_blocks_.items()) own(block_owner, b, "a free block that is also in use");
   for (const Writeback& w : wbs_)
-    if (w.discard) take(block_used, w.block, "a discarded write-back block in use");
+    if (w.discard) own(block_owner, w.block, "a discarded write-back block in use");
   for (uint32_t s = 0; s < c_.persistent_slots; ++s)
-    if (!slot_used[s]) broken("a persistent slot neither free nor held");
+    if (!slot_owner[s]) broken("a persistent slot neither free nor held");
   for (uint32_t b = 0; b < c_.blocks; ++b)
-    if (!block_used[b]) broken("a block neither free nor held");
+    if (!block_owner[b]) broken("a block neither free nor held");
 }
 
 }  // namespace tsb

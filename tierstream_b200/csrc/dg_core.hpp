@@ -287,14 +287,66 @@ class SlotCache {
 
  private:
   static constexpr uint32_t kNil = 0xffffffffu;
+  // An intrusive doubly linked list of keys (front: the most recent); the links live in the list, one pair per key.
+  class KeyList {
+   public:
+    void reset(uint32_t keys) {
+      link_.assign(keys, Link{});
+      front_ = back_ = kNil;
+    }
+    bool has(uint32_t k) const { return link_[k].in; }
+    uint32_t front() const { return front_; }
+    uint32_t back() const { return back_; }
+    uint32_t older(uint32_t k) const { return link_[k].next; }  // toward the back
+    uint32_t newer(uint32_t k) const { return link_[k].prev; }  // toward the front
+    void push_front(uint32_t k) { insert(k, kNil, front_); }
+    void push_back(uint32_t k) { insert(k, back_, kNil); }
+    void erase(uint32_t k) {
+      Link& l = link_[k];
+      (l.prev == kNil ? front_ : link_[l.prev].next) = l.next;
+      (l.next == kNil ? back_ : link_[l.next].prev) = l.prev;
+      l = Link{};
+    }
+
+   private:
+    struct Link {
+      uint32_t prev = kNil, next = kNil;
+      bool in = false;
+    };
+    void insert(uint32_t k, uint32_t before, uint32_t after) {
+      link_[k] = Link{before, after, true};
+      (before == kNil ? front_ : link_[before].next) = k;
+      (after == kNil ? back_ : link_[after].prev) = k;
+    }
+    std::vector<Link> link_;
+    uint32_t front_ = kNil, back_ = kNil;
+  };
+  // Free slots or blocks: a stack whose next is the one returned last (at open, the lowest index).
+  class LifoPool {
+   public:
+    void clear() { v_.clear(); }
+    void fill_down(int32_t hi, int32_t lo) {  // hi - 1 .. lo pushed in that order: lo is taken first
+      v_.clear();
+      for (int32_t i = hi; i-- > lo;) v_.push_back(i);
+    }
+    void give(int32_t i) { v_.push_back(i); }
+    int32_t take() {
+      const int32_t i = v_.back();
+      v_.pop_back();
+      return i;
+    }
+    bool empty() const { return v_.empty(); }
+    size_t size() const { return v_.size(); }
+    const std::vector<int32_t>& items() const { return v_; }
+
+   private:
+    std::vector<int32_t> v_;
+  };
   struct Entry {
     Home home = Home::Host;
     int32_t slot = -1, block = -1;
-    uint32_t prev = kNil, next = kNil;
-    bool listed = false, wb_pending = false, via_pf = false, used = false;
+    bool wb_pending = false, via_pf = false, used = false;
     bool backed = false;  // a device unit whose block still holds its bytes (inclusive share)
-    bool in_hlist = false;           // file tier: in the pinned homes' recency list
-    uint32_t hprev = kNil, hnext = kNil;
     uint64_t demand_epoch = 0, lru_stamp = 0;  // scored: the last token that routed it; its recency list position
     void* pf_done = nullptr;
   };
@@ -311,9 +363,30 @@ class SlotCache {
     uint32_t parts_done;
     uint64_t bytes;
   };
+  // The state reset_open restores.
+  struct OpenState {
+    CacheConfig cfg;
+    std::vector<Entry> ent;
+    std::vector<int32_t> table;
+    LifoPool slots, blocks;
+    KeyList recent, homes;
+    uint32_t on_device = 0, on_file = 0;
+    uint64_t stamp = 0;
+  };
 
-  void unlink(uint32_t k);
-  void push_front(uint32_t k);
+  // ---- the recency list and the pinned homes' list ----
+  void touch(uint32_t k);          // to the recency front (a fresh stamp when scored)
+  void leave_device(uint32_t k);   // out of the recency list, entry withdrawn
+  void home_push(uint32_t k, bool cold = false);  // file tier: a pinned home, most (cold: least) recently homed
+  void home_erase(uint32_t k);
+  void recycle(void*& ev);         // an event back to the pool
+  void count_fetch(uint32_t g, bool prefetch, int delta = 1);
+  void count_evicted(uint32_t k);
+  // one event of gated layer g: the context's total and the layer's own count
+  void bump(uint32_t g, uint64_t CacheStats::*total, uint64_t LayerCounts::*layer) {
+    ++(st_.*total);
+    ++(lc_[g].*layer);
+  }
   // ---- file reads in flight ----
   struct Pending {
     uint32_t key;
@@ -331,6 +404,7 @@ class SlotCache {
   void drain_layer(uint32_t g, const uint32_t* ids, uint32_t n);
   void finish_pending(const Pending& p);
   void undo_pending(const Pending& p);
+  void make_room_for_read();
   // ---- scored eviction ----
   struct ScoreCand {
     uint64_t s, epoch, stamp;
@@ -364,16 +438,15 @@ class SlotCache {
   void* record_front(bool discard);
   void* finish_front();
   void force_free_slot();
+  void settle_writebacks(const char* what);
   int32_t bank_slot(uint32_t g);
+  bool resurrect(uint32_t k);
   void to_lower(uint32_t k, bool cold = false);
-  void hpush(uint32_t k);
-  void hpush_tail(uint32_t k);
   bool clean_now() const { return c_.clean_evict && c_.disk_tier && free_blocks_.empty(); }
   void count_clean() {
     ++st_.clean_drops;
     st_.clean_drop_bytes += unit_bytes_;
   }
-  void hunlink(uint32_t k);
   // the least recently homed pinned unit not in `skip` to its file; count: a disk drop of the boundary
   bool drop_host_lru(const std::vector<uint8_t>* skip = nullptr, bool count = true);
   int32_t take_stage();
@@ -384,23 +457,23 @@ class SlotCache {
   void apply_wb_defer();
   [[noreturn]] void broken(const std::string& what) const;
 
-  CacheConfig c_, open_c_;
+  CacheConfig c_;
   Mover* m_;
   std::vector<uint32_t> base_;
   uint32_t keys_ = 0, slots_ = 0, bank_first_ = 0;
-  std::vector<Entry> e_, open_e_;
-  std::vector<int32_t> table_, open_table_;
-  std::vector<int32_t> free_slots_, free_blocks_, open_free_slots_, open_free_blocks_;
-  uint32_t head_ = kNil, tail_ = kNil, on_device_ = 0, backed_ = 0;
-  uint32_t open_head_ = kNil, open_tail_ = kNil, open_on_device_ = 0;
-  uint32_t hhead_ = kNil, htail_ = kNil, on_file_ = 0, open_hhead_ = kNil, open_htail_ = kNil, open_on_file_ = 0;
+  std::vector<Entry> e_;
+  std::vector<int32_t> table_;
+  LifoPool free_slots_, free_blocks_;
+  KeyList recent_, homes_;  // homes_: the file tier's pinned homes, front = most recently homed
+  uint32_t on_device_ = 0, backed_ = 0, on_file_ = 0;
+  OpenState open_;
   uint32_t stage_next_ = 0;
   std::vector<void*> stage_ev_;  // per staging buffer: its last copy's event
   std::vector<Pending> pending_;  // file reads in flight, oldest first
   uint64_t entries_ = 0;          // public calls so far (a read ended in a later one was carried)
   std::vector<LayerScore> sc_;
   std::vector<uint8_t> run_;
-  uint64_t epoch_ = 0, stamp_ = 0, open_stamp_ = 0;
+  uint64_t epoch_ = 0, stamp_ = 0;
   std::vector<ScoreCand> select_heap_;
   std::vector<double> rs_;         // placement rounds: the decayed counts
   std::vector<uint32_t> rhits_;    // the tokens that routed each unit since the last round

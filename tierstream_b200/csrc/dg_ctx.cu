@@ -15,6 +15,7 @@
 #include <immintrin.h>
 
 #include <algorithm>
+#include <numeric>
 #include <atomic>
 #include <chrono>
 #include <cstdio>
@@ -117,186 +118,220 @@ struct Layout {
   std::string provenance;
 };
 
-Layout make_layout(const Desc& d, const Plan& p, const ss_options& o, const PeerTier* peer) {
-  auto refuse = [](ss_status st, const std::string& why) { fail(st, "device-gated: " + why); };
-  const ss_budget& b = p.budget;
-  if (b.tier_mode != SS_TIER_MODE_EXCLUSIVE) refuse(SS_E_INVALID, "needs tier_mode EXCLUSIVE");
-  if (b.pinned_backing) refuse(SS_E_INVALID, "pinned_backing is refused (each unit has one home)");
-  if (o.policy != SS_POLICY_LRU && o.policy != SS_POLICY_SCORED && o.policy != SS_POLICY_SCORED_AUTO)
-    refuse(SS_E_INVALID, "policy must be LRU, SCORED or SCORED_AUTO");
-  if ((o.dg_score_profile_len || o.dg_score_profile) && o.policy == SS_POLICY_LRU)
-    refuse(SS_E_INVALID, "dg_score_profile needs policy SCORED");
-  if (o.pin_planned) refuse(SS_E_INVALID, "needs pin_planned = 0 (planned residents are a warm start)");
-  if (!o.fill_residents) refuse(SS_E_INVALID, "needs fill_residents = 1 (a resident's slot is its only copy)");
-  if (o.readahead_units) refuse(SS_E_INVALID, "readahead_units must be 0 (no gated unit is read from its file)");
-  if (o.spec_persistent) refuse(SS_E_INVALID, "spec_persistent is refused (prediction is the service's)");
-  if (o.dg_max_ids < 1 || o.dg_max_ids > dev::kMaxIds) refuse(SS_E_INVALID, "dg_max_ids must be 1..64 (rows x top_k)");
-  if (o.dg_wait_timeout_ms < 1) refuse(SS_E_INVALID, "dg_wait_timeout_ms must be >= 1");
-  if (o.dg_wb_defer > 1) refuse(SS_E_INVALID, "dg_wb_defer must be 0 or 1");
-  if (o.dg_wb_stream > 1) refuse(SS_E_INVALID, "dg_wb_stream must be 0 or 1");
-  // the file tier, as the reference checks its options (dg_layout.cpp:200-207)
+[[noreturn]] void dg_refuse(ss_status st, const std::string& why) { fail(st, "device-gated: " + why); }
+
+// The options an open checks before it reads the descriptor. Every SS_E_INVALID refusal comes before the
+// SS_E_UNSUPPORTED ones, so a set of options with several faults gets the reference's status (dg_layout.cpp:183-215).
+void check_dg_options(const ss_budget& b, const ss_options& o, const PeerTier* peer) {
   constexpr uint32_t kQueueAuto = 0xFFFFFFFFu;
-  if (o.dg_disk_tier > 1 || o.dg_disk_prefetch > 1) refuse(SS_E_INVALID, "dg_disk_tier / dg_disk_prefetch must be 0 or 1");
-  if (!o.dg_disk_tier && (o.dg_disk_prefetch || o.dg_disk_staging || (o.dg_disk_queue && o.dg_disk_queue != kQueueAuto)))
-    refuse(SS_E_INVALID, "dg_disk_prefetch / dg_disk_staging / dg_disk_queue need dg_disk_tier = 1");
-  if (o.dg_disk_staging > 256) refuse(SS_E_INVALID, "dg_disk_staging must be 0..256");
-  if (o.dg_disk_queue > 64 && o.dg_disk_queue != kQueueAuto)
-    refuse(SS_E_INVALID, "dg_disk_queue must be 0..64 or SS_DG_DISK_QUEUE_AUTO");
-  if (o.dg_disk_tier && peer) refuse(SS_E_UNSUPPORTED, "the file tier with the peer tier is not in this build");
-  // the reference's opt-in policies this build has (dg_layout.cpp:208-215)
-  if (o.dg_no_admit > 1) refuse(SS_E_INVALID, "dg_no_admit must be 0 or 1");
-  if (o.dg_clean_evict > 1) refuse(SS_E_INVALID, "dg_clean_evict must be 0 or 1");
-  if (o.dg_pf_revert_unused > 1) refuse(SS_E_INVALID, "dg_pf_revert_unused must be 0 or 1");
-  if (o.dg_pf_strict_admit > 1) refuse(SS_E_INVALID, "dg_pf_strict_admit must be 0 or 1");
+  struct Need {
+    bool ok;
+    const char* why;
+  };
+  const Need invalid[] = {
+      {b.tier_mode == SS_TIER_MODE_EXCLUSIVE, "needs tier_mode EXCLUSIVE"},
+      {!b.pinned_backing, "pinned_backing is refused (each unit has one home)"},
+      {o.policy == SS_POLICY_LRU || o.policy == SS_POLICY_SCORED || o.policy == SS_POLICY_SCORED_AUTO,
+       "policy must be LRU, SCORED or SCORED_AUTO"},
+      {!(o.dg_score_profile_len || o.dg_score_profile) || o.policy != SS_POLICY_LRU,
+       "dg_score_profile needs policy SCORED"},
+      {!o.pin_planned, "needs pin_planned = 0 (planned residents are a warm start)"},
+      {o.fill_residents != 0, "needs fill_residents = 1 (a resident's slot is its only copy)"},
+      {!o.readahead_units, "readahead_units must be 0 (no gated unit is read from its file)"},
+      {!o.spec_persistent, "spec_persistent is refused (prediction is the service's)"},
+      {o.dg_max_ids >= 1 && o.dg_max_ids <= dev::kMaxIds, "dg_max_ids must be 1..64 (rows x top_k)"},
+      {o.dg_wait_timeout_ms >= 1, "dg_wait_timeout_ms must be >= 1"},
+      {o.dg_disk_tier <= 1 && o.dg_disk_prefetch <= 1, "dg_disk_tier / dg_disk_prefetch must be 0 or 1"},
+      {o.dg_disk_tier || !(o.dg_disk_prefetch || o.dg_disk_staging || (o.dg_disk_queue && o.dg_disk_queue != kQueueAuto)),
+       "dg_disk_prefetch / dg_disk_staging / dg_disk_queue need dg_disk_tier = 1"},
+      {o.dg_disk_staging <= 256, "dg_disk_staging must be 0..256"},
+      {o.dg_disk_queue <= 64 || o.dg_disk_queue == kQueueAuto, "dg_disk_queue must be 0..64 or SS_DG_DISK_QUEUE_AUTO"},
+  };
+  for (const Need& n : invalid)
+    if (!n.ok) dg_refuse(SS_E_INVALID, n.why);
+  // switches that are 0 or 1
+  const std::pair<uint32_t, const char*> flags[] = {
+      {o.dg_wb_defer, "dg_wb_defer"},         {o.dg_wb_stream, "dg_wb_stream"},
+      {o.dg_no_admit, "dg_no_admit"},         {o.dg_clean_evict, "dg_clean_evict"},
+      {o.dg_pf_revert_unused, "dg_pf_revert_unused"}, {o.dg_pf_strict_admit, "dg_pf_strict_admit"},
+  };
+  for (const auto& f : flags)
+    if (f.first > 1) dg_refuse(SS_E_INVALID, std::string(f.second) + " must be 0 or 1");
+  if (o.dg_disk_tier && peer) dg_refuse(SS_E_UNSUPPORTED, "the file tier with the peer tier is not in this build");
   if (o.dg_landing_blocks || o.dg_bank_keep || o.dg_disk_queue_adapt || o.dg_prior_len)
-    refuse(SS_E_UNSUPPORTED, "an opt-in device-gated policy of the reference that is not in this build is set");
-  Layout x;
-  x.B = o.dg_max_ids;
+    dg_refuse(SS_E_UNSUPPORTED, "an opt-in device-gated policy of the reference that is not in this build is set");
+}
+
+// The gated layers (every layer with units; each must be streamable) and the one part shape they share: the arena
+// is a single array of slots, each the concatenation of the parts (each a multiple of 256 bytes).
+void gate_layers(const Desc& d, Layout& x) {
   x.ordinal.assign(d.layers.size(), -1);
-  const Layer* shape = nullptr;
   for (size_t L = 0; L < d.layers.size(); ++L) {
     const Layer& l = d.layers[L];
     if (l.n_units == 0) continue;
-    if (!l.streamable)
-      refuse(SS_E_UNSUPPORTED, "layer " + std::to_string(l.index) + " has non-streamable units (every unit is gated)");
-    if (!shape) {
-      shape = &l;
+    const std::string name = "layer " + std::to_string(l.index);
+    if (!l.streamable) dg_refuse(SS_E_UNSUPPORTED, name + " has non-streamable units (every unit is gated)");
+    if (x.gated.empty()) {  // the shape
       if (l.parts.size() > SS_DG_MAX_PARTS)
-        refuse(SS_E_UNSUPPORTED, "more than " + std::to_string(SS_DG_MAX_PARTS) + " parts per unit");
-      uint64_t off = 0;
+        dg_refuse(SS_E_UNSUPPORTED, "more than " + std::to_string(SS_DG_MAX_PARTS) + " parts per unit");
+      uint64_t at = 0;
       for (const Part& part : l.parts) {
-        if (part.bytes % 256 != 0)
-          refuse(SS_E_UNSUPPORTED, "part " + part.name + " is " + std::to_string(part.bytes) +
-                                       " bytes, not a multiple of 256 (the arena stride equals the part bytes)");
+        if (part.bytes % 256)
+          dg_refuse(SS_E_UNSUPPORTED, "part " + part.name + " is " + std::to_string(part.bytes) +
+                                          " bytes, not a multiple of 256 (the arena stride equals the part bytes)");
+        x.part_offset.push_back(at);
         x.part_bytes.push_back(part.bytes);
-        x.part_offset.push_back(off);
-        off += part.bytes;
+        at += part.bytes;
       }
       x.unit_bytes = l.unit_bytes;
     } else {
-      bool same = l.parts.size() == shape->parts.size();
-      for (size_t i = 0; same && i < l.parts.size(); ++i) same = l.parts[i].bytes == shape->parts[i].bytes;
-      if (!same) refuse(SS_E_UNSUPPORTED, "layer " + std::to_string(l.index) + " has another part shape (one arena)");
+      const std::vector<Part>& first = d.layers[size_t(x.gated[0])].parts;
+      const bool same = std::equal(l.parts.begin(), l.parts.end(), first.begin(), first.end(),
+                                   [](const Part& a, const Part& c) { return a.bytes == c.bytes; });
+      if (!same) dg_refuse(SS_E_UNSUPPORTED, name + " has another part shape (one arena)");
     }
     x.ordinal[L] = int(x.gated.size());
     x.gated.push_back(int(L));
   }
-  if (x.gated.empty()) refuse(SS_E_INVALID, "the descriptor has no streamable units");
-  const uint32_t G = uint32_t(x.gated.size());
+  if (x.gated.empty()) dg_refuse(SS_E_INVALID, "the descriptor has no streamable units");
   x.host_stride = host_stride(x.unit_bytes);
+}
+
+// Every gated unit's home from the plan (resident, pinned, or with the file tier its file), keys in descriptor order;
+// the spare slots the plan billed: per layer its dynamic slots, never more than its non-resident units.
+void place_homes(const Desc& d, const Plan& p, const ss_options& o, Layout& x) {
+  const bool files = o.dg_disk_tier != 0;
+  uint64_t key = 0;
   x.unit_base.assign(1, 0);
-  uint64_t keys = 0;
-  for (uint32_t g = 0; g < G; ++g) {
-    const Layer& l = d.layers[size_t(x.gated[g])];
-    uint32_t planned = 0;
-    for (int u = 0; u < l.n_units; ++u) {
-      const uint8_t t = p.tier[size_t(d.unit_base[size_t(x.gated[g])] + u)];
-      if (t == SS_TIER_RESIDENT) {
-        x.residents.push_back(uint32_t(keys + uint64_t(u)));
-        ++planned;
-      } else if (t == SS_TIER_PINNED) {
-        ++x.P;
-      } else if (t == SS_TIER_DISK && o.dg_disk_tier) {
-        ++x.F;
+  for (int L : x.gated) {
+    const Layer& l = d.layers[size_t(L)];
+    const size_t first = size_t(d.unit_base[size_t(L)]);
+    uint32_t resident_here = 0;
+    for (int u = 0; u < l.n_units; ++u, ++key) {
+      const uint8_t tier = p.tier[first + size_t(u)];
+      const bool to_file = files && tier == SS_TIER_DISK;
+      if (tier == SS_TIER_RESIDENT) {
+        x.residents.push_back(uint32_t(key));
+        ++resident_here;
+      } else if (tier == SS_TIER_PINNED || to_file) {
+        ++(to_file ? x.F : x.P);
       } else {
-        refuse(SS_E_CAPACITY, "unit (" + std::to_string(l.index) + ", " + std::to_string(u) +
-                                  ") is not resident or pinned (no gated unit is read from its file)");
+        dg_refuse(SS_E_CAPACITY, "unit (" + std::to_string(l.index) + ", " + std::to_string(u) +
+                                     ") is not resident or pinned (no gated unit is read from its file)");
       }
-      if (o.dg_disk_tier) x.disk.push_back(t == SS_TIER_DISK ? 1 : 0);
+      if (files) x.disk.push_back(uint8_t(to_file));
     }
-    x.D += std::min<uint32_t>(b.dynamic_slots_per_layer, uint32_t(l.n_units) - planned);
-    keys += uint64_t(l.n_units);
-    require(keys < 0x7fffffffull, SS_E_INVALID, "device-gated: more than 2^31 - 1 gated units");
-    x.unit_base.push_back(uint32_t(keys));
+    x.D += std::min<uint32_t>(p.budget.dynamic_slots_per_layer, uint32_t(l.n_units) - resident_here);
+    require(key < 0x7fffffffull, SS_E_INVALID, "device-gated: more than 2^31 - 1 gated units");
+    x.unit_base.push_back(uint32_t(key));
   }
-  x.keys = uint32_t(keys);
+  x.keys = uint32_t(key);
   x.R = uint32_t(x.residents.size());
-  x.disk_tier = o.dg_disk_tier != 0;
+  // file reads in flight and their staging buffers (dg_layout.cpp:159-181, one location per source here): AUTO is
+  // 4 bounded by an explicit staging count, an explicit 0 means 1; staging defaults to 8 buffers
+  x.disk_tier = files;
   x.disk_prefetch = o.dg_disk_prefetch != 0;
-  // reads in flight and staging buffers, resolved as the reference resolves them (dg_layout.cpp:159-181): AUTO is
-  // clamp(3 x locations, 4, 8) bounded by an explicit staging count (one location per source here: no stripes), the
-  // staging default 8 raised to it; an explicit queue 0 means 1
-  if (x.disk_tier && o.dg_disk_queue == kQueueAuto) {
-    x.disk_queue = o.dg_disk_staging ? std::min<uint32_t>(4, o.dg_disk_staging) : 4u;
-    x.S = o.dg_disk_staging ? o.dg_disk_staging : std::max<uint32_t>(8, x.disk_queue);
-  } else if (x.disk_tier) {
-    x.disk_queue = o.dg_disk_queue ? o.dg_disk_queue : 1u;
-    x.S = o.dg_disk_staging ? o.dg_disk_staging : 8u;
+  if (files) {
+    const uint32_t staging = o.dg_disk_staging;
+    x.disk_queue = o.dg_disk_queue == 0xFFFFFFFFu ? std::min<uint32_t>(4, staging ? staging : 4)
+                                                  : std::max<uint32_t>(1, o.dg_disk_queue);
+    x.S = staging ? staging : 8u;
   }
-  // scored eviction: the weights, the per-layer bound and the profile (every rule of its format, against this
-  // descriptor's identity), as the reference resolves them (dg_layout.cpp:349-371)
-  if (o.policy == SS_POLICY_SCORED || o.policy == SS_POLICY_SCORED_AUTO) {
-    x.scored = true;
-    x.scored_auto = o.policy == SS_POLICY_SCORED_AUTO;
-    if (o.dg_score_w_trans || o.dg_score_w_freq || o.dg_score_w_recency) {
-      if (o.dg_score_w_trans > 1000 || o.dg_score_w_freq > 1000 || o.dg_score_w_recency > 1000 ||
-          o.dg_score_w_trans + o.dg_score_w_freq + o.dg_score_w_recency != 1000)
-        refuse(SS_E_INVALID, "dg_score_w_trans / _freq / _recency must each be 0..1000 and sum to 1000");
-      x.w_trans = o.dg_score_w_trans;
-      x.w_freq = o.dg_score_w_freq;
-      x.w_rec = o.dg_score_w_recency;
-    }
-    std::vector<uint32_t> units;
-    for (int L : x.gated) {
-      units.push_back(uint32_t(d.layers[size_t(L)].n_units));
-      if (units.back() > 65536)
-        refuse(SS_E_INVALID, "scored eviction needs at most 65536 units per gated layer (layer " +
-                                 std::to_string(d.layers[size_t(L)].index) + ")");
-    }
-    if (o.dg_score_profile_len || o.dg_score_profile) {
-      if (!o.dg_score_profile || !o.dg_score_profile_len)
-        refuse(SS_E_INVALID, "dg_score_profile and dg_score_profile_len must be given together");
-      ScoreProfile prof = check_score_profile(o.dg_score_profile, o.dg_score_profile_len, units,
-                                              score_identity(d, x.gated));
-      x.profile = std::move(prof.cells);
-      x.provenance = std::move(prof.provenance);
-    }
+}
+
+// Scored eviction (dg_layout.cpp:349-371): the three weights (per mille, summing to 1000, or all 0 for the
+// defaults), at most 65536 units per gated layer, and a profile checked against this descriptor's identity.
+void resolve_scoring(const Desc& d, const ss_options& o, Layout& x) {
+  if (o.policy != SS_POLICY_SCORED && o.policy != SS_POLICY_SCORED_AUTO) return;
+  x.scored = true;
+  x.scored_auto = o.policy == SS_POLICY_SCORED_AUTO;
+  const uint32_t w[3] = {o.dg_score_w_trans, o.dg_score_w_freq, o.dg_score_w_recency};
+  if (w[0] || w[1] || w[2]) {
+    const bool each = w[0] <= 1000 && w[1] <= 1000 && w[2] <= 1000;
+    if (!each || w[0] + w[1] + w[2] != 1000)
+      dg_refuse(SS_E_INVALID, "dg_score_w_trans / _freq / _recency must each be 0..1000 and sum to 1000");
+    x.w_trans = w[0];
+    x.w_freq = w[1];
+    x.w_rec = w[2];
   }
+  std::vector<uint32_t> units;
+  units.reserve(x.gated.size());
+  for (int L : x.gated) {
+    const Layer& l = d.layers[size_t(L)];
+    if (l.n_units > 65536)
+      dg_refuse(SS_E_INVALID, "scored eviction needs at most 65536 units per gated layer (layer " +
+                                  std::to_string(l.index) + ")");
+    units.push_back(uint32_t(l.n_units));
+  }
+  if (!o.dg_score_profile && !o.dg_score_profile_len) return;
+  if (!o.dg_score_profile || !o.dg_score_profile_len)
+    dg_refuse(SS_E_INVALID, "dg_score_profile and dg_score_profile_len must be given together");
+  ScoreProfile prof = check_score_profile(o.dg_score_profile, o.dg_score_profile_len, units, score_identity(d, x.gated));
+  x.profile = std::move(prof.cells);
+  x.provenance = std::move(prof.provenance);
+}
+
+// Slots and blocks: R + D persistent slots (D the billed spare slots, or dg_spare_slots), then two banks of B and the
+// guard; P + Q pinned blocks (Q the plan's spare blocks, at least one kept free of the inclusive share); and the two
+// admissions - the arena against the device cap less the margin, the staging units against the pinned budget.
+void size_arena(const Desc& d, const Plan& p, const ss_options& o, const PeerTier* peer, Layout& x) {
+  const ss_budget& b = p.budget;
   if (o.dg_spare_slots) {
     if (o.dg_spare_slots > x.P + x.F)
-      refuse(SS_E_INVALID, "dg_spare_slots " + std::to_string(o.dg_spare_slots) + " above the non-resident units (" +
-                               std::to_string(x.P + x.F) + ")");
+      dg_refuse(SS_E_INVALID, "dg_spare_slots " + std::to_string(o.dg_spare_slots) + " above the non-resident units (" +
+                                  std::to_string(x.P + x.F) + ")");
     x.D = o.dg_spare_slots;
   }
-  if (x.D < 1)
-    refuse(SS_E_INVALID, "needs dynamic_slots_per_layer > 0 or dg_spare_slots > 0 (the spare slots)");
+  if (x.D == 0) dg_refuse(SS_E_INVALID, "needs dynamic_slots_per_layer > 0 or dg_spare_slots > 0 (the spare slots)");
+  const uint64_t want_ring = 2ull * x.B + 1;
   const uint64_t stride = d.unit_stride(x.gated[0]);
-  uint32_t ring_slots = 0;
+  uint32_t ring_slots = 0;  // (of the ring class with the gated units' stride)
   for (const RingClass& rc : p.rings)
     if (rc.stride == stride) ring_slots = rc.slots;
-  if (uint64_t(ring_slots) < 2ull * x.B + 1)
-    refuse(SS_E_CAPACITY, "the plan bills " + std::to_string(ring_slots) + " ring slots, the banks and the guard need " +
-                              std::to_string(2 * x.B + 1) + " (set ring_slots = 2 x dg_max_ids + 1)");
+  if (ring_slots < want_ring)
+    dg_refuse(SS_E_CAPACITY, "the plan bills " + std::to_string(ring_slots) + " ring slots, the banks and the guard need " +
+                                 std::to_string(want_ring) + " (set ring_slots = 2 x dg_max_ids + 1)");
   for (const SpareClass& sc : p.spares)
     if (sc.block_bytes == x.host_stride) x.Q = sc.blocks;
-  if (x.Q < 1)
-    refuse(SS_E_CAPACITY, "the plan granted no spare blocks (host_spare_units asked " +
-                              std::to_string(b.host_spare_units) + "): a write-back needs a free block");
+  if (x.Q == 0)
+    dg_refuse(SS_E_CAPACITY, "the plan granted no spare blocks (host_spare_units asked " +
+                                 std::to_string(b.host_spare_units) + "): a write-back needs a free block");
   x.blocks = x.P + x.Q;
-  // the inclusive share comes out of the spare blocks: at least one stays for write-backs
   x.I = o.dg_inclusive_blocks;
   if (x.I && x.I >= x.Q)
-    refuse(SS_E_CAPACITY, "dg_inclusive_blocks " + std::to_string(x.I) + " must stay below the spare blocks (" +
-                              std::to_string(x.Q) + "): raise host_spare_units by the inclusive share");
+    dg_refuse(SS_E_CAPACITY, "dg_inclusive_blocks " + std::to_string(x.I) + " must stay below the spare blocks (" +
+                                 std::to_string(x.Q) + "): raise host_spare_units by the inclusive share");
   x.persistent_slots = x.R + x.D;
-  const uint64_t S = uint64_t(x.persistent_slots) + 2ull * x.B + 1;
-  require(S < 0x7fffffffull, SS_E_INVALID, "device-gated: more than 2^31 - 1 slots");
-  x.slots = uint32_t(S);
+  const uint64_t all_slots = uint64_t(x.persistent_slots) + want_ring;
+  require(all_slots < 0x7fffffffull, SS_E_INVALID, "device-gated: more than 2^31 - 1 slots");
+  x.slots = uint32_t(all_slots);
   x.guard_slot = x.slots - 1;
-  // device admission: what the arena needs in place of what the plan billed for the gated slots
-  uint64_t per_slot = 0;
-  for (uint64_t pb : x.part_bytes) per_slot += pb;
-  const uint64_t need = S * per_slot + keys * 4 + 4096;
+  // device: the arena and the published table in place of what the plan billed for gated slots
+  const uint64_t slot_bytes = std::accumulate(x.part_bytes.begin(), x.part_bytes.end(), uint64_t(0));
+  const uint64_t arena = all_slots * slot_bytes + uint64_t(x.keys) * 4 + 4096;
   const uint64_t billed = p.resident + p.dynamic + p.ring;
-  const uint64_t limit = p.cap > p.margin ? p.cap - p.margin : 0;
-  const uint64_t other = p.peak >= billed ? p.peak - billed : 0;
-  if (other + need > limit)
-    refuse(SS_E_CAPACITY, "the arena needs " + std::to_string(need) + " bytes where the plan billed " +
-                              std::to_string(billed) + "; with the rest of the plan that is above the cap - margin");
-  const bool no_blocks = peer && peer->all_owned;  // every unit in a store: no pinned block is allocated
-  if (!no_blocks && p.pinned + (1ull + x.S) * x.host_stride + (uint64_t(1) << 20) > b.host_pinned_bytes)
-    refuse(SS_E_CAPACITY, "the plan's pinned bytes plus the staging units and the mapped control area exceed the host "
-                          "budget (" + std::to_string(b.host_pinned_bytes) + ")");
+  const uint64_t rest = p.peak >= billed ? p.peak - billed : 0;
+  const uint64_t room = p.cap > p.margin ? p.cap - p.margin : 0;
+  if (rest + arena > room)
+    dg_refuse(SS_E_CAPACITY, "the arena needs " + std::to_string(arena) + " bytes where the plan billed " +
+                                 std::to_string(billed) + "; with the rest of the plan that is above the cap - margin");
+  // host: the plan's pinned bytes, one reset unit and S staging units, and 1 MiB of mapped control words (none of
+  // the blocks when every unit lives in a peer store)
+  const bool no_blocks = peer && peer->all_owned;
+  const uint64_t pinned = p.pinned + (1ull + x.S) * x.host_stride + (uint64_t(1) << 20);
+  if (!no_blocks && pinned > b.host_pinned_bytes)
+    dg_refuse(SS_E_CAPACITY, "the plan's pinned bytes plus the staging units and the mapped control area exceed the "
+                             "host budget (" + std::to_string(b.host_pinned_bytes) + ")");
+}
+
+Layout make_layout(const Desc& d, const Plan& p, const ss_options& o, const PeerTier* peer) {
+  check_dg_options(p.budget, o, peer);
+  Layout x;
+  x.B = o.dg_max_ids;
+  gate_layers(d, x);
+  place_homes(d, p, o, x);
+  resolve_scoring(d, o, x);
+  size_arena(d, p, o, peer, x);
   return x;
 }
 
@@ -1207,13 +1242,7 @@ class CudaDgContext final : public DgContext {
     require(!in_token_, SS_E_INVALID, "ss_seed: between tokens in device-gated mode");
     const int g = gated_index(layer);
     require(g >= 0, SS_E_INVALID, "ss_seed: layer " + std::to_string(layer) + " is not gated");
-    require(n >= 0 && (n == 0 || units), SS_E_INVALID, "ss_seed: bad arguments");
-    std::vector<uint32_t> keys;
-    for (int i = 0; i < n; ++i) {
-      require(units[i] >= 0 && uint32_t(units[i]) < core_->units(uint32_t(g)), SS_E_INVALID, "ss_seed: unit out of range");
-      keys.push_back(core_->key(uint32_t(g), uint32_t(units[i])));
-    }
-    core_->seed(keys);
+    core_->seed(keys_of(g, units, n, "ss_seed", "unit"));
   }
 
   void check_unit(int layer, int unit) override {
@@ -1223,27 +1252,36 @@ class CudaDgContext final : public DgContext {
     require(unit >= 0 && uint32_t(unit) < core_->units(uint32_t(g)), SS_E_INVALID, "ss_check_unit: unit out of range");
     core_->drain();
     const uint32_t k = core_->key(uint32_t(g), uint32_t(unit));
-    if (core_->home(k) == SlotCache::Home::File) {  // its only copy is its file
-      core_->check();
-      return;
+    std::vector<char> held;
+    if (live_copy(k, held)) {  // (a unit whose only copy is its file has nothing to compare)
+      std::vector<char> source(held.size());
+      read_unit(layer, unit, source.data());
+      require(held == source, SS_E_HASH,
+              "check_unit: the bytes of (" + std::to_string(layer) + ", " + std::to_string(unit) +
+                  ") differ from the source");
     }
-    std::vector<char> got(size_t(x_.unit_bytes)), want(size_t(x_.unit_bytes));
-    if (core_->slot_of(k) >= 0 &&
-        (core_->home(k) == SlotCache::Home::Device || core_->home(k) == SlotCache::Home::Evicting)) {
-      for (size_t p = 0; p < x_.part_bytes.size(); ++p)
-        ck(cudaMemcpy(got.data() + x_.part_offset[p], bufs_.arena[p] + uint64_t(core_->slot_of(k)) * x_.part_bytes[p],
-                      size_t(x_.part_bytes[p]), cudaMemcpyDeviceToHost),
-           "cudaMemcpy (check)");
-    } else if (peer_ && peer_->owned(k)) {  // a Host home whose bytes live in a store
-      ck(cudaMemcpy(got.data(), peer_->src(k, x_.unit_bytes), got.size(), cudaMemcpyDefault), "cudaMemcpy (check)");
-    } else {
-      std::memcpy(got.data(), bufs_.blocks[size_t(core_->block_of(k))], got.size());
-    }
-    read_unit(layer, unit, want.data());
-    require(std::memcmp(got.data(), want.data(), got.size()) == 0, SS_E_HASH,
-            "check_unit: the bytes of (" + std::to_string(layer) + ", " + std::to_string(unit) +
-                ") differ from the source");
     core_->check();
+  }
+
+  // The bytes of key k's live copy into `out`: its slot while on the device (or being evicted from it), else its
+  // peer store or its pinned block; false when its only copy is its file.
+  bool live_copy(uint32_t k, std::vector<char>& out) {
+    const SlotCache::Home home = core_->home(k);
+    if (home == SlotCache::Home::File) return false;
+    out.resize(size_t(x_.unit_bytes));
+    const int32_t slot = core_->slot_of(k);
+    if (slot >= 0 && (home == SlotCache::Home::Device || home == SlotCache::Home::Evicting)) {
+      for (size_t part = 0; part < x_.part_bytes.size(); ++part) {
+        const char* src = bufs_.arena[part] + uint64_t(slot) * x_.part_bytes[part];
+        ck(cudaMemcpy(out.data() + x_.part_offset[part], src, size_t(x_.part_bytes[part]), cudaMemcpyDeviceToHost),
+           "cudaMemcpy (check)");
+      }
+    } else if (peer_ && peer_->owned(k)) {
+      ck(cudaMemcpy(out.data(), peer_->src(k, x_.unit_bytes), out.size(), cudaMemcpyDefault), "cudaMemcpy (check)");
+    } else {
+      std::memcpy(out.data(), bufs_.blocks[size_t(core_->block_of(k))], out.size());
+    }
+    return true;
   }
 
   void device_view(ss_dg_device_view* v) const override {
@@ -1295,13 +1333,7 @@ class CudaDgContext final : public DgContext {
   void keep(int g, const int32_t* ids, int n) override {
     require(!in_token_, SS_E_INVALID, "ss_dg_keep: between tokens only");
     check_g(g, "ss_dg_keep");
-    require(n >= 0 && (n == 0 || ids), SS_E_INVALID, "ss_dg_keep: bad arguments");
-    std::vector<uint32_t> keys;
-    for (int i = 0; i < n; ++i) {
-      require(ids[i] >= 0 && uint32_t(ids[i]) < core_->units(uint32_t(g)), SS_E_INVALID, "ss_dg_keep: unit out of range");
-      keys.push_back(core_->key(uint32_t(g), uint32_t(ids[i])));
-    }
-    keep_[size_t(g)] = std::move(keys);
+    keep_[size_t(g)] = keys_of(g, ids, n, "ss_dg_keep", "unit");
     held_[size_t(g)] = 0;  // a plain keep: g is exported again
   }
   // ss_dg_make_resident: the units of gated layer g all on the device and kept there; g is not exported while held (the
@@ -1309,31 +1341,25 @@ class CudaDgContext final : public DgContext {
   void make_resident(int g, const int32_t* ids, int n) override {
     require(!in_token_, SS_E_INVALID, "ss_dg_make_resident: between tokens only");
     check_g(g, "ss_dg_make_resident");
-    require(n >= 0 && (n == 0 || ids), SS_E_INVALID, "ss_dg_make_resident: bad arguments");
-    if (n == 0) {
+    std::vector<uint32_t> keys = keys_of(g, ids, n, "ss_dg_make_resident", "id");
+    if (keys.empty()) {  // a release
       keep_[size_t(g)].clear();
       held_[size_t(g)] = 0;
       return;
     }
-    std::vector<uint32_t> units, keys;
-    for (int i = 0; i < n; ++i) {
-      require(ids[i] >= 0 && uint32_t(ids[i]) < core_->units(uint32_t(g)), SS_E_INVALID,
-              "ss_dg_make_resident: id out of range");
-      units.push_back(uint32_t(ids[i]));
-      keys.push_back(core_->key(uint32_t(g), uint32_t(ids[i])));
-    }
+    std::vector<uint32_t> units(ids, ids + n);  // (checked: 0 <= id < units of g)
     core_->make_resident(uint32_t(g), units, keep_all());  // a refusal changes nothing (g keeps its former keep)
     keep_[size_t(g)] = std::move(keys);
     held_[size_t(g)] = 1;
   }
   uint32_t residency(ss_dg_unit* out, uint32_t cap) override {
     require(!in_token_, SS_E_INVALID, "ss_dg_residency: between tokens only");
-    const std::vector<uint32_t> keys = core_->residency();
-    const uint32_t n = uint32_t(std::min<size_t>(keys.size(), cap));
-    for (uint32_t i = 0; i < n; ++i) {
-      const uint32_t g = core_->gated_of(keys[i]);
-      out[i] = ss_dg_unit{int32_t(g), int32_t(keys[i] - core_->key(g, 0))};
-    }
+    const std::vector<uint32_t> keys = core_->residency();  // most recent first
+    auto as_unit = [this](uint32_t k) {
+      const uint32_t g = core_->gated_of(k);
+      return ss_dg_unit{int32_t(g), int32_t(k - core_->key(g, 0))};
+    };
+    std::transform(keys.begin(), keys.begin() + std::min<size_t>(keys.size(), cap), out, as_unit);
     return uint32_t(keys.size());
   }
   void set_peer(const PeerTier& t) override {
@@ -1684,6 +1710,17 @@ class CudaDgContext final : public DgContext {
   void check_g(int g, const char* fn) const {
     require(g >= 0 && size_t(g) < x_.gated.size(), SS_E_INVALID, std::string(fn) + ": gated layer out of range");
   }
+  // The keys of units `ids[0..n)` of gated layer g, each checked (`fn`: the entry point; `what`: "unit" or "id").
+  std::vector<uint32_t> keys_of(int g, const int32_t* ids, int n, const char* fn, const char* what) const {
+    require(n >= 0 && (n == 0 || ids), SS_E_INVALID, std::string(fn) + ": bad arguments");
+    const uint32_t limit = core_->units(uint32_t(g));
+    std::vector<uint32_t> keys(static_cast<size_t>(n));
+    for (int i = 0; i < n; ++i) {
+      require(ids[i] >= 0 && uint32_t(ids[i]) < limit, SS_E_INVALID, std::string(fn) + ": " + what + " out of range");
+      keys[size_t(i)] = core_->key(uint32_t(g), uint32_t(ids[i]));
+    }
+    return keys;
+  }
   std::vector<uint32_t> keep_all() const {
     std::vector<uint32_t> all;
     for (const auto& k : keep_) all.insert(all.end(), k.begin(), k.end());
@@ -1811,22 +1848,20 @@ class CudaDgContext final : public DgContext {
     carve(prec_b, &m_.prec, &dev_.prec);
     carve(size_t(G) * 4, &m_.flag, &dev_.flag);
     carve(size_t(G) * 4, &m_.pflag, &dev_.pflag);
-    uint32_t *words_h = nullptr, *words_d = nullptr;
-    carve(7 * 4, &words_h, &words_d);
-    m_.done = words_h;
-    m_.err_code = words_h + 1;
-    m_.err_aux = words_h + 2;
-    m_.host_abort = words_h + 3;
-    m_.host_seq = words_h + 4;
-    m_.began = words_h + 5;
-    m_.err_count = words_h + 6;
-    dev_.done = words_d;
-    dev_.m_err_code = words_d + 1;
-    dev_.m_err_aux = words_d + 2;
-    dev_.host_abort = words_d + 3;
-    dev_.host_seq = words_d + 4;
-    dev_.began = words_d + 5;
-    dev_.m_err_count = words_d + 6;
+    {  // single control words, each seen by the host (m_) and the device (dev_) at its two addresses
+      uint32_t** host_side[] = {&m_.done, &m_.err_code, &m_.err_aux, &m_.host_abort, &m_.host_seq, &m_.began,
+                                &m_.err_count};
+      uint32_t** device_side[] = {&dev_.done, &dev_.m_err_code, &dev_.m_err_aux, &dev_.host_abort, &dev_.host_seq,
+                                  &dev_.began, &dev_.m_err_count};
+      constexpr size_t kWords = sizeof host_side / sizeof host_side[0];
+      static_assert(kWords == sizeof device_side / sizeof device_side[0], "one device address per host word");
+      uint32_t *words_h = nullptr, *words_d = nullptr;
+      carve(kWords * 4, &words_h, &words_d);
+      for (size_t w = 0; w < kWords; ++w) {
+        *host_side[w] = words_h + w;
+        *device_side[w] = words_d + w;
+      }
+    }
     uint32_t *chk_h = nullptr, *chk_d = nullptr;
     carve(check_b, &chk_h, &chk_d);
     bad_flag_h_ = chk_h;

@@ -25,6 +25,7 @@
 #include <condition_variable>
 #include <cstdlib>
 #include <cstring>
+#include <iterator>
 #include <deque>
 #include <memory>
 #include <mutex>
@@ -290,19 +291,20 @@ class HostCtx final : public HostContext {
       ck(cudaStreamWaitEvent(es, s.ready_ev, 0), "cudaStreamWaitEvent (ready)");
       s.ready_wait = false;
     }
+    // groups: the hits (on the device already) first, then the units fetched for this layer, most routed rows first,
+    // in chunks of group_units (one chunk when 0), each chunk in unit order
     std::vector<int32_t> fetched;
-    for (int32_t u : s.routed)
-      if (s.job[size_t(u)]) fetched.push_back(u);
+    std::copy_if(s.routed.begin(), s.routed.end(), std::back_inserter(fetched),
+                 [&](int32_t u) { return bool(s.job[size_t(u)]); });
     std::stable_sort(fetched.begin(), fetched.end(),
                      [&](int32_t a, int32_t b) { return s.count[size_t(a)] > s.count[size_t(b)]; });
-    s.groups.clear();
-    s.groups.push_back(s.hits);
-    const size_t gsz = o_.group_units ? o_.group_units : std::max<size_t>(fetched.size(), 1);
-    for (size_t k = 0; k < fetched.size(); k += gsz) {
-      std::vector<int32_t> g(fetched.begin() + std::ptrdiff_t(k),
-                             fetched.begin() + std::ptrdiff_t(std::min(fetched.size(), k + gsz)));
-      std::sort(g.begin(), g.end());
-      s.groups.push_back(g);
+    s.groups.assign(1, s.hits);
+    const size_t chunk = o_.group_units ? size_t(o_.group_units) : std::max<size_t>(fetched.size(), 1);
+    for (auto from = fetched.begin(); from != fetched.end();) {
+      const auto to = from + std::ptrdiff_t(std::min<size_t>(chunk, size_t(fetched.end() - from)));
+      s.groups.emplace_back(from, to);
+      std::sort(s.groups.back().begin(), s.groups.back().end());
+      from = to;
     }
     if (wait_all) {
       const uint64_t t0 = now_ns();
@@ -578,19 +580,15 @@ class HostCtx final : public HostContext {
     int version = 0;
   };
 
+  // a += b, counter by counter (the struct is twelve uint64_t counters and nothing else)
   static void add(ss_layer_stats& a, const ss_layer_stats& b) {
-    a.routed += b.routed;
-    a.hits += b.hits;
-    a.admitted += b.admitted;
-    a.transient += b.transient;
-    a.evicted += b.evicted;
-    a.prefetched += b.prefetched;
-    a.spec_issued += b.spec_issued;
-    a.spec_used += b.spec_used;
-    a.spec_dropped += b.spec_dropped;
-    a.bytes_pinned += b.bytes_pinned;
-    a.bytes_disk += b.bytes_disk;
-    a.wait_ns += b.wait_ns;
+    constexpr size_t kCounters = sizeof(ss_layer_stats) / sizeof(uint64_t);
+    static_assert(kCounters == 12 && sizeof(ss_layer_stats) == kCounters * sizeof(uint64_t), "counters only");
+    uint64_t sum[kCounters], more[kCounters];
+    std::memcpy(sum, &a, sizeof sum);
+    std::memcpy(more, &b, sizeof more);
+    for (size_t i = 0; i < kCounters; ++i) sum[i] += more[i];
+    std::memcpy(&a, sum, sizeof sum);
   }
   int64_t gidx(int layer, int unit) const { return d_.unit_base[size_t(layer)] + unit; }
   uint64_t stride(int layer) const { return d_.unit_stride(layer); }
@@ -1000,24 +998,25 @@ class HostCtx final : public HostContext {
     std::vector<int32_t> to_admit, misses;  // misses: prefetched this forward or not resident (SCORED's recency)
     std::vector<char> busy(size_t(l.n_units), 0);
     for (int u = 0; u < l.n_units; ++u) {
-      if (s.loc[size_t(u)] != kNone) busy[size_t(u)] = 1;
-      if (!s.count[size_t(u)] || plan_.tier[size_t(gidx(layer, u))] == SS_TIER_PAIR) continue;
-      busy[size_t(u)] = 1;
+      const size_t x = size_t(u);
+      const bool in_flight = s.loc[x] != kNone;  // fetched or prefetched in this forward already
+      const bool wanted = s.count[x] != 0 && plan_.tier[size_t(gidx(layer, u))] != SS_TIER_PAIR;
+      busy[x] = char(in_flight || wanted);
+      if (!wanted) continue;
       s.routed.push_back(u);
-      if (s.loc[size_t(u)] != kNone) {  // prefetched this forward
-        if (s.spec_unclaimed[size_t(u)]) {
-          s.spec_unclaimed[size_t(u)] = 0;
-          ++st.spec_used;
-          if (s.job[size_t(u)]) promote(s.job[size_t(u)]);
-        } else {
-          ++st.prefetched;
-        }
-        misses.push_back(u);
-      } else if (s.rs->slot(u) >= 0) {
+      if (!in_flight && s.rs->slot(u) >= 0) {  // resident: a hit
         s.hits.push_back(u);
-      } else {
+        continue;
+      }
+      misses.push_back(u);  // (SCORED's recency: prefetched in this forward, or not resident)
+      if (!in_flight) {
         to_admit.push_back(u);
-        misses.push_back(u);
+      } else if (s.spec_unclaimed[x]) {  // a speculative read the routes now claim: it moves up the queue
+        s.spec_unclaimed[x] = 0;
+        ++st.spec_used;
+        if (s.job[x]) promote(s.job[x]);
+      } else {
+        ++st.prefetched;
       }
     }
     st.routed += s.routed.size();

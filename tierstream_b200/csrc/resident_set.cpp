@@ -1,199 +1,214 @@
+// The host forward mode's per-layer resident set; the rules are stated in resident_set.hpp.
 #include "resident_set.hpp"
 
 #include <algorithm>
 #include <numeric>
+#include <tuple>
 
 #include "errors.hpp"
 
 namespace tsb {
 
+namespace {
+
+// The scored cut's order: a higher score first, then the later last use, then the lower unit id.
+struct CutKey {
+  double score;
+  uint64_t stamp;
+  int32_t unit;
+  bool before(const CutKey& o) const {
+    return std::make_tuple(o.score, o.stamp, unit) < std::make_tuple(score, stamp, o.unit);
+  }
+};
+
+std::vector<int32_t> ascending_unique(std::vector<int32_t> v) {
+  std::sort(v.begin(), v.end());
+  v.erase(std::unique(v.begin(), v.end()), v.end());
+  return v;
+}
+
+}  // namespace
+
 ResidentSet::ResidentSet(int n_units, int capacity, bool scored, uint32_t window)
-    : n_units_(n_units), scored_(scored), window_(window) {
+    : n_units_(n_units), scored_(scored), window_(window ? window : 16) {
   require(capacity >= 0 && capacity <= n_units, SS_E_INVALID, "resident set: capacity must be 0..n_units");
-  slot_of_.assign(size_t(n_units), -1);
-  unit_in_.assign(size_t(capacity), -1);
-  pinned_.assign(size_t(capacity), 0);
-  last_use_.assign(size_t(n_units), 0);
+  slots_.resize(size_t(capacity));
+  home_.assign(size_t(n_units), -1);
+  free_bits_.assign((size_t(capacity) + 63) / 64, 0);
+  for (int s = 0; s < capacity; ++s) free_bits_[size_t(s) / 64] |= uint64_t(1) << (s % 64);
+  stamp_.assign(size_t(n_units), 0);
   if (scored_) {
-    trans_.assign(size_t(n_units) * size_t(n_units), 0);
-    trans_n_.assign(size_t(n_units), 0);
-    freq_.assign(size_t(n_units), 0);
+    h_.pair.assign(size_t(n_units) * size_t(n_units), 0);
+    h_.from.assign(size_t(n_units), 0);
+    h_.in_ring.assign(size_t(n_units), 0);
+    h_.ring.resize(window_);
   }
 }
 
-// In double precision, in this order of operations (the decisions compare these values exactly).
+int ResidentSet::first_free() const {
+  for (size_t w = 0; w < free_bits_.size(); ++w)
+    if (free_bits_[w]) return int(w * 64 + size_t(__builtin_ctzll(free_bits_[w])));
+  return -1;
+}
+
+void ResidentSet::occupy(int slot, int32_t unit, bool pin) {
+  slots_[size_t(slot)] = Slot{unit, pin};
+  home_[size_t(unit)] = slot;
+  free_bits_[size_t(slot) / 64] &= ~(uint64_t(1) << (slot % 64));
+  ++occupied_;
+}
+
+void ResidentSet::vacate(int slot) {
+  Slot& s = slots_[size_t(slot)];
+  home_[size_t(s.unit)] = -1;
+  s = Slot{};
+  free_bits_[size_t(slot) / 64] |= uint64_t(1) << (slot % 64);
+  --occupied_;
+}
+
+// The terms and their order of operations are fixed: the cut compares these doubles exactly.
 double ResidentSet::score(int unit) const {
   if (!scored_) return 0.0;
   double trans = 0.0;
-  if (!prev_.empty()) {
-    for (int32_t p : prev_) {
-      const uint32_t n = trans_n_[size_t(p)];
-      if (n) trans += double(trans_[size_t(p) * size_t(n_units_) + size_t(unit)]) / double(n);
+  if (!h_.last.empty()) {
+    for (int32_t p : h_.last) {
+      const uint32_t n = h_.from[size_t(p)];
+      if (n) trans += double(h_.pair[size_t(p) * size_t(n_units_) + size_t(unit)]) / double(n);
     }
-    trans /= double(prev_.size());
+    trans /= double(h_.last.size());
   }
-  const double freq = recent_.empty() ? 0.0 : double(freq_[size_t(unit)]) / double(recent_.size());
-  const uint64_t lu = last_use_[size_t(unit)];
-  const double rec = lu ? 1.0 / (1.0 + double(tick_ - lu)) : 0.0;
+  const double freq = h_.count ? double(h_.in_ring[size_t(unit)]) / double(h_.count) : 0.0;
+  const uint64_t st = stamp_[size_t(unit)];
+  const double rec = st ? 1.0 / (1.0 + double(now_ - st)) : 0.0;
   return 0.7 * trans + 0.2 * freq + 0.1 * rec;
 }
 
 int ResidentSet::place(int unit, bool pin) {
   require(unit >= 0 && unit < n_units_, SS_E_INVALID, "resident set: unit out of range");
-  int& s = slot_of_[size_t(unit)];
-  if (s >= 0) {
-    if (pin) pinned_[size_t(s)] = 1;
-    return s;
+  if (const int at = home_[size_t(unit)]; at >= 0) {
+    if (pin) slots_[size_t(at)].pinned = true;
+    return at;
   }
-  const auto it = std::find(unit_in_.begin(), unit_in_.end(), -1);
-  if (it == unit_in_.end()) return -1;
-  s = int32_t(it - unit_in_.begin());
-  *it = unit;
-  pinned_[size_t(s)] = pin;
-  ++n_resident_;
+  const int s = first_free();
+  if (s >= 0) occupy(s, unit, pin);
   return s;
 }
 
 void ResidentSet::drop(int unit) {
-  const int s = slot_of_[size_t(unit)];
-  if (s < 0) return;
-  unit_in_[size_t(s)] = -1;
-  pinned_[size_t(s)] = 0;
-  slot_of_[size_t(unit)] = -1;
-  --n_resident_;
-}
-
-int ResidentSet::lru_victim(const std::vector<char>& keep) const {
-  int best = -1;
-  for (size_t s = 0; s < unit_in_.size(); ++s) {
-    const int32_t u = unit_in_[s];
-    if (u < 0 || pinned_[s] || keep[size_t(u)]) continue;
-    if (best >= 0) {
-      const int32_t b = unit_in_[size_t(best)];
-      const uint64_t lu = last_use_[size_t(u)], lb = last_use_[size_t(b)];
-      if (!(lu < lb || (lu == lb && u < b))) continue;
-    }
-    best = int(s);
-  }
-  return best;
+  if (const int at = home_[size_t(unit)]; at >= 0) vacate(at);
 }
 
 Admission ResidentSet::admit(const std::vector<int32_t>& routed_in, const std::vector<char>& busy, bool admit_misses,
                              int max_evictions) {
-  Admission a;
-  std::vector<int32_t> routed = routed_in;
-  std::sort(routed.begin(), routed.end());
-  routed.erase(std::unique(routed.begin(), routed.end()), routed.end());
-  std::vector<char> keep(size_t(n_units_), 0);
+  Admission out;
+  const std::vector<int32_t> routed = ascending_unique(routed_in);
+  // protected this forward: the routed units and the busy ones (their copies are in flight)
+  std::vector<char> hold(size_t(n_units_), 0);
   std::vector<int32_t> misses;
   for (int32_t u : routed) {
     require(u >= 0 && u < n_units_, SS_E_INVALID, "routes: unit id out of range");
-    keep[size_t(u)] = 1;
-    (slot_of_[size_t(u)] >= 0 ? a.hits : misses).push_back(u);
+    hold[size_t(u)] = 1;
+    if (home_[size_t(u)] >= 0) out.hits.push_back(u);
+    else misses.push_back(u);
   }
-  for (size_t u = 0; u < busy.size() && u < keep.size(); ++u)
-    if (busy[u]) keep[u] = 1;
-  if (!admit_misses || unit_in_.empty()) {
-    a.transient = misses;
-    return a;
+  for (size_t u = 0; u < std::min(busy.size(), hold.size()); ++u) hold[u] |= busy[u] ? 1 : 0;
+  if (!admit_misses || slots_.empty()) {
+    out.transient = misses;
+    return out;
   }
-  std::vector<int32_t> take = misses;  // the misses that get a slot, in admission order
+  // the residents that may be evicted: unpinned and not held
+  std::vector<int32_t> evictable;
+  int n_free = 0;
+  for (const Slot& s : slots_) {
+    if (s.unit < 0) ++n_free;
+    else if (!s.pinned && !hold[size_t(s.unit)]) evictable.push_back(s.unit);
+  }
+  std::vector<int32_t> order = misses;  // the misses that get a slot, in admission order (LRU: ascending ids)
   if (scored_) {
-    // the scored cut: the unpinned residents outside this forward and the misses compete for the rows they can hold
-    struct Cand {
-      int32_t unit;
-      double score;
-      uint64_t last;
-      bool resident;
-    };
-    std::vector<Cand> comp;
-    size_t free_slots = 0;
-    for (size_t s = 0; s < unit_in_.size(); ++s) {
-      const int32_t u = unit_in_[s];
-      if (u < 0) ++free_slots;
-      else if (!pinned_[s] && !keep[size_t(u)]) comp.push_back({u, score(u), last_use_[size_t(u)], true});
+    // the cut: evictable residents and misses ranked together for the n_free + evictable rows; misses inside are
+    // admitted in rank order, and only residents outside may be evicted
+    std::vector<CutKey> keys;
+    for (int32_t u : evictable) keys.push_back({score(u), stamp_[size_t(u)], u});
+    const size_t n_res = keys.size(), rows = size_t(n_free) + n_res;
+    for (int32_t u : misses) keys.push_back({score(u), stamp_[size_t(u)], u});
+    std::vector<size_t> rank(keys.size());
+    std::iota(rank.begin(), rank.end(), size_t(0));
+    std::sort(rank.begin(), rank.end(), [&](size_t a, size_t b) { return keys[a].before(keys[b]); });
+    order.clear();
+    std::vector<char> outside(size_t(n_units_), 0);
+    for (size_t r = 0; r < rank.size(); ++r) {
+      const bool is_miss = rank[r] >= n_res;
+      if (r < rows && is_miss) order.push_back(keys[rank[r]].unit);
+      if (r >= rows && !is_miss) outside[size_t(keys[rank[r]].unit)] = 1;
     }
-    const size_t rows = free_slots + comp.size();
-    for (int32_t u : misses) comp.push_back({u, score(u), last_use_[size_t(u)], false});
-    std::sort(comp.begin(), comp.end(), [](const Cand& x, const Cand& y) {
-      if (x.score != y.score) return x.score > y.score;
-      if (x.last != y.last) return x.last > y.last;
-      return x.unit < y.unit;
-    });
-    take.clear();
-    for (size_t i = 0; i < comp.size() && i < rows; ++i)
-      if (!comp[i].resident) take.push_back(comp[i].unit);
-    std::vector<char> below(size_t(n_units_), 0);  // residents below the cut: the only eviction candidates
-    for (size_t i = rows; i < comp.size(); ++i)
-      if (comp[i].resident) below[size_t(comp[i].unit)] = 1;
-    for (size_t u = 0; u < keep.size(); ++u)
-      if (!below[u] && slot_of_[u] >= 0) keep[u] = 1;
+    evictable.erase(std::remove_if(evictable.begin(), evictable.end(),
+                                   [&](int32_t u) { return !outside[size_t(u)]; }),
+                    evictable.end());
   }
-  std::vector<char> taken(size_t(n_units_), 0);
-  std::vector<std::pair<int32_t, int32_t>> adm, ev;  // (unit, slot)
-  for (int32_t u : take) {
-    int s = -1;
-    const auto it = std::find(unit_in_.begin(), unit_in_.end(), -1);
-    if (it != unit_in_.end()) {
-      s = int(it - unit_in_.begin());
-    } else {
-      if (max_evictions >= 0 && int(ev.size()) >= max_evictions) {
-        ++a.deferred;
+  // victims in eviction order: the least recent first, ties to the lower id
+  std::sort(evictable.begin(), evictable.end(), [&](int32_t a, int32_t b) {
+    return std::make_pair(stamp_[size_t(a)], a) < std::make_pair(stamp_[size_t(b)], b);
+  });
+  size_t next_victim = 0;
+  std::vector<char> got(size_t(n_units_), 0);
+  std::vector<std::pair<int32_t, int32_t>> admitted, evicted;  // (unit, slot)
+  for (int32_t u : order) {
+    int s = first_free();
+    if (s < 0) {
+      if (max_evictions >= 0 && int(evicted.size()) >= max_evictions) {
+        ++out.deferred;  // no free slot and no eviction allowed: stays transient
         continue;
       }
-      s = lru_victim(keep);
-      if (s < 0) break;  // everything resident is pinned or in use this forward
-      const int32_t old = unit_in_[size_t(s)];
-      slot_of_[size_t(old)] = -1;
-      ev.push_back({old, s});
-      --n_resident_;
+      if (next_victim == evictable.size()) break;  // everything resident is pinned or held this forward
+      const int32_t v = evictable[next_victim++];
+      s = home_[size_t(v)];
+      vacate(s);
+      evicted.push_back({v, s});
     }
-    unit_in_[size_t(s)] = u;
-    pinned_[size_t(s)] = 0;
-    slot_of_[size_t(u)] = s;
-    keep[size_t(u)] = 1;
-    taken[size_t(u)] = 1;
-    ++n_resident_;
-    adm.push_back({u, s});
+    occupy(s, u, false);
+    got[size_t(u)] = 1;
+    admitted.push_back({u, s});
   }
   for (int32_t u : misses)
-    if (!taken[size_t(u)]) a.transient.push_back(u);
-  std::sort(adm.begin(), adm.end());
-  std::sort(ev.begin(), ev.end());
-  for (const auto& x : adm) {
-    a.admitted.push_back(x.first);
-    a.slot_of.push_back(x.second);
+    if (!got[size_t(u)]) out.transient.push_back(u);
+  std::sort(admitted.begin(), admitted.end());
+  std::sort(evicted.begin(), evicted.end());
+  for (const auto& [u, s] : admitted) {
+    out.admitted.push_back(u);
+    out.slot_of.push_back(s);
   }
-  for (const auto& x : ev) {
-    a.evicted.push_back(x.first);
-    a.evicted_slot.push_back(x.second);
+  for (const auto& [u, s] : evicted) {
+    out.evicted.push_back(u);
+    out.evicted_slot.push_back(s);
   }
-  return a;
+  return out;
 }
 
 void ResidentSet::observe(const std::vector<int32_t>& routed_in, const std::vector<int32_t>& misses) {
-  ++tick_;
+  const std::vector<int32_t> routed = ascending_unique(routed_in);
+  ++now_;
   if (!scored_) {
-    for (int32_t u : routed_in) last_use_[size_t(u)] = tick_;
+    for (int32_t u : routed) stamp_[size_t(u)] = now_;
     return;
   }
-  std::vector<int32_t> routed = routed_in;
-  std::sort(routed.begin(), routed.end());
-  routed.erase(std::unique(routed.begin(), routed.end()), routed.end());
-  for (int32_t u : misses) last_use_[size_t(u)] = tick_;  // a miss and a first use refresh recency, a hit does not
-  for (int32_t u : routed)
-    if (last_use_[size_t(u)] == 0) last_use_[size_t(u)] = tick_;
-  for (int32_t p : prev_) {
-    ++trans_n_[size_t(p)];
-    for (int32_t u : routed) ++trans_[size_t(p) * size_t(n_units_) + size_t(u)];
+  // SCORED: a miss (admitted or not) and a first use refresh a unit's recency; a hit does not
+  for (int32_t u : misses) stamp_[size_t(u)] = now_;
+  for (int32_t u : routed) stamp_[size_t(u)] = stamp_[size_t(u)] ? stamp_[size_t(u)] : now_;
+  for (int32_t p : h_.last) {
+    h_.from[size_t(p)] += 1;
+    uint32_t* row = h_.pair.data() + size_t(p) * size_t(n_units_);
+    for (int32_t u : routed) row[u] += 1;
   }
-  prev_ = routed;
-  recent_.push_back(routed);
-  for (int32_t u : routed) ++freq_[size_t(u)];
-  if (recent_.size() > window_) {
-    for (int32_t u : recent_.front()) --freq_[size_t(u)];
-    recent_.pop_front();
+  h_.last = routed;
+  // the window ring: the oldest forward leaves once the ring is full
+  if (h_.count == window_) {
+    for (int32_t u : h_.ring[h_.head]) h_.in_ring[size_t(u)] -= 1;
+  } else {
+    ++h_.count;
   }
+  h_.ring[h_.head] = routed;
+  for (int32_t u : routed) h_.in_ring[size_t(u)] += 1;
+  h_.head = (h_.head + 1) % window_;
 }
 
 }  // namespace tsb

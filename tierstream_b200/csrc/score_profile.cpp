@@ -20,38 +20,33 @@ constexpr uint32_t kK[64] = {
     0xc67178f2};
 
 inline uint32_t rotr(uint32_t x, int n) { return (x >> n) | (x << (32 - n)); }
+inline uint32_t sigma0(uint32_t x) { return rotr(x, 7) ^ rotr(x, 18) ^ (x >> 3); }
+inline uint32_t sigma1(uint32_t x) { return rotr(x, 17) ^ rotr(x, 19) ^ (x >> 10); }
+inline uint32_t Sigma0(uint32_t x) { return rotr(x, 2) ^ rotr(x, 13) ^ rotr(x, 22); }
+inline uint32_t Sigma1(uint32_t x) { return rotr(x, 6) ^ rotr(x, 11) ^ rotr(x, 25); }
+inline uint32_t choose(uint32_t x, uint32_t y, uint32_t z) { return z ^ (x & (y ^ z)); }
+inline uint32_t majority(uint32_t x, uint32_t y, uint32_t z) { return (x & y) | (z & (x | y)); }
 
-void compress(uint32_t h[8], const unsigned char* block) {
+// One 64-byte block into the state. The eight working variables live in a ring: in round t, variable i (a = 0 ..
+// h = 7) is v[(i - t) & 7], so a round writes only the two that change - d's register gains T1 (it is the next
+// round's e) and h's register takes T1 + T2 (the next round's a) - and nothing is shifted.
+void compress(uint32_t state[8], const unsigned char* block) {
   uint32_t w[64];
-  for (int t = 0; t < 16; ++t)
-    w[t] = uint32_t(block[4 * t]) << 24 | uint32_t(block[4 * t + 1]) << 16 | uint32_t(block[4 * t + 2]) << 8 |
-           uint32_t(block[4 * t + 3]);
-  for (int t = 16; t < 64; ++t) {
-    const uint32_t s0 = rotr(w[t - 15], 7) ^ rotr(w[t - 15], 18) ^ (w[t - 15] >> 3);
-    const uint32_t s1 = rotr(w[t - 2], 17) ^ rotr(w[t - 2], 19) ^ (w[t - 2] >> 10);
-    w[t] = w[t - 16] + s0 + w[t - 7] + s1;
+  for (int t = 0; t < 16; ++t) {
+    w[t] = 0;
+    for (int k = 0; k < 4; ++k) w[t] = (w[t] << 8) | block[4 * t + k];  // big-endian words
   }
-  uint32_t a = h[0], b = h[1], c = h[2], d = h[3], e = h[4], f = h[5], g = h[6], k = h[7];
+  for (int t = 16; t < 64; ++t) w[t] = sigma1(w[t - 2]) + w[t - 7] + sigma0(w[t - 15]) + w[t - 16];
+  uint32_t v[8];
+  std::memcpy(v, state, sizeof v);
   for (int t = 0; t < 64; ++t) {
-    const uint32_t t1 = k + (rotr(e, 6) ^ rotr(e, 11) ^ rotr(e, 25)) + ((e & f) ^ (~e & g)) + kK[t] + w[t];
-    const uint32_t t2 = (rotr(a, 2) ^ rotr(a, 13) ^ rotr(a, 22)) + ((a & b) ^ (a & c) ^ (b & c));
-    k = g;
-    g = f;
-    f = e;
-    e = d + t1;
-    d = c;
-    c = b;
-    b = a;
-    a = t1 + t2;
+    auto var = [&](int i) -> uint32_t& { return v[(i - t) & 7]; };
+    const uint32_t t1 = var(7) + Sigma1(var(4)) + choose(var(4), var(5), var(6)) + kK[t] + w[t];
+    const uint32_t t2 = Sigma0(var(0)) + majority(var(0), var(1), var(2));
+    var(3) += t1;
+    var(7) = t1 + t2;
   }
-  h[0] += a;
-  h[1] += b;
-  h[2] += c;
-  h[3] += d;
-  h[4] += e;
-  h[5] += f;
-  h[6] += g;
-  h[7] += k;
+  for (int i = 0; i < 8; ++i) state[i] += v[i];  // (after 64 rounds the ring is back at offset 0)
 }
 
 void put32(std::string& b, uint32_t v) {
@@ -101,41 +96,51 @@ std::string score_identity(const Desc& d, const std::vector<int>& gated) {
   return sha256(b.data(), b.size());
 }
 
+// TSSCPRF1: magic[8], u32 version (1), u32 n_gated, u32 units per gated layer, identity[32], u32 prov_len,
+// prov[prov_len], per gated layer units^2 u32 counts, sha256[32] of everything before it. Checked front to back,
+// each field against this context before the next is read.
 ScoreProfile check_score_profile(const void* data, uint64_t len, const std::vector<uint32_t>& units,
                                  const std::string& identity) {
   if (!data) bad("null data");
-  const auto* p = static_cast<const unsigned char*>(data);
-  const uint64_t G = units.size();
+  const auto* bytes = static_cast<const unsigned char*>(data);
+  const uint64_t n_gated = units.size();
+  const uint64_t head = 8 + 4 + 4 + 4 * n_gated + 32 + 4;  // through prov_len
+  if (len < head) bad("truncated header (" + std::to_string(len) + " bytes)");
+  uint64_t at = 0;
+  auto word = [&] {
+    const uint32_t v = get32(bytes + at);
+    at += 4;
+    return v;
+  };
+  if (std::memcmp(bytes, "TSSCPRF1", 8) != 0) bad("bad magic");
+  at = 8;
+  if (const uint32_t version = word(); version != 1) bad("unsupported version " + std::to_string(version));
+  if (const uint32_t n = word(); n != n_gated)
+    bad("n_gated " + std::to_string(n) + " != the context's " + std::to_string(n_gated));
+  for (size_t g = 0; g < units.size(); ++g)
+    if (const uint32_t u = word(); u != units[g])
+      bad("units of gated layer " + std::to_string(g) + " are " + std::to_string(u) + ", the context has " +
+          std::to_string(units[g]));
+  const unsigned char* id = bytes + at;
+  at += 32;
+  const uint32_t prov = word();
+  if (prov > 4096) bad("provenance longer than 4096 bytes");
   uint64_t cells = 0;
   for (uint32_t u : units) cells += uint64_t(u) * u;  // (units <= 65536 per layer: checked by the open)
-  const uint64_t fixed = 8 + 4 + 4 + 4 * G + 32 + 4;  // through prov_len
-  if (len < fixed) bad("truncated header (" + std::to_string(len) + " bytes)");
-  if (std::memcmp(p, "TSSCPRF1", 8) != 0) bad("bad magic");
-  if (get32(p + 8) != 1) bad("unsupported version " + std::to_string(get32(p + 8)));
-  if (get32(p + 12) != G) bad("n_gated " + std::to_string(get32(p + 12)) + " != the context's " + std::to_string(G));
-  for (uint64_t g = 0; g < G; ++g)
-    if (get32(p + 16 + 4 * g) != units[size_t(g)])
-      bad("units of gated layer " + std::to_string(g) + " are " + std::to_string(get32(p + 16 + 4 * g)) +
-          ", the context has " + std::to_string(units[size_t(g)]));
-  const uint64_t at_id = 16 + 4 * G;
-  const uint32_t prov = get32(p + at_id + 32);
-  if (prov > 4096) bad("provenance longer than 4096 bytes");
-  const uint64_t header = fixed + prov, want = header + 4 * cells + 32;
+  const uint64_t want = head + prov + 4 * cells + 32;
   if (len != want) bad("size " + std::to_string(len) + " != " + std::to_string(want) + " (header + cells + checksum)");
-  if (identity.size() != 32 || std::memcmp(p + at_id, identity.data(), 32) != 0)
+  if (identity.size() != 32 || std::memcmp(id, identity.data(), 32) != 0)
     bad("identity mismatch (another model, layer set or descriptor)");
-  if (sha256(p, size_t(len - 32)) != std::string(reinterpret_cast<const char*>(p + len - 32), 32))
+  if (sha256(bytes, size_t(len - 32)) != std::string(reinterpret_cast<const char*>(bytes + len - 32), 32))
     bad("checksum mismatch");
   ScoreProfile out;
-  out.provenance.assign(reinterpret_cast<const char*>(p + fixed), prov);
-  const unsigned char* c = p + header;
-  out.cells.resize(size_t(G));
-  for (uint64_t g = 0; g < G; ++g) {
-    out.cells[size_t(g)].resize(size_t(units[size_t(g)]) * units[size_t(g)]);
-    for (uint32_t& v : out.cells[size_t(g)]) {
-      v = get32(c);
-      c += 4;
-    }
+  out.provenance.assign(reinterpret_cast<const char*>(bytes + at), prov);
+  at += prov;
+  out.cells.reserve(units.size());
+  for (uint32_t u : units) {
+    std::vector<uint32_t> layer(size_t(u) * u);
+    for (uint32_t& v : layer) v = word();
+    out.cells.push_back(std::move(layer));
   }
   return out;
 }
