@@ -50,8 +50,8 @@ QWEN3 = dict(LAYERS=94, UNITS=128, PART=12582912, TOP_K=8, ZIPF=1.2, RESIDENTS=9
 def args_():
     p = argparse.ArgumentParser()
     p.add_argument("--gpus", type=int, default=1)
-    p.add_argument("--steps", type=int, default=64)
-    p.add_argument("--warmup", type=int, default=8)
+    p.add_argument("--steps", type=int, default=None, help="timed steps (default: 64; c1-host 64, llama3-70b-host 12)")
+    p.add_argument("--warmup", type=int, default=None, help="warm-up steps (default: 8; llama3-70b-host 3)")
     p.add_argument("--impl", default="tierstream", choices=["tierstream", "reference"])
     p.add_argument("--copy-mode", default=os.environ.get("TSB_COPY_MODE", "auto"), choices=["auto", "kernel", "ce"])
     p.add_argument("--wb-defer", type=int, default=0,
@@ -80,9 +80,14 @@ def args_():
                    help="device-gated eviction policy (ss_options.policy)")
     p.add_argument("--round-every", type=int, default=0,
                    help="a placement round (ss_dg_round, defaults) after every N tokens, inside the timed steps")
-    p.add_argument("--workload", default="mixtral-8x7b-dg", choices=["mixtral-8x7b-dg", "qwen3-235b-a22b-peer"],
+    p.add_argument("--workload", default="mixtral-8x7b-dg",
+                   choices=["mixtral-8x7b-dg", "qwen3-235b-a22b-peer", "c1-host", "llama3-70b-host"],
                    help="mixtral-8x7b-dg: BASELINE configs[1] (default); qwen3-235b-a22b-peer: configs[4], the peer "
-                        "tier on 4 or more GPUs")
+                        "tier on 4 or more GPUs; c1-host and llama3-70b-host: configs[0] and [2] in the host forward "
+                        "mode on one GPU (tierstream_b200/host_bench.py)")
+    p.add_argument("--ref-threads", type=int, default=0,
+                   help="host workloads, --impl reference: the reference's reader_threads, pinned to that many CPUs "
+                        "(0: every CPU this process may use, at most 64)")
     p.add_argument("--layers", type=int, default=0,
                    help="qwen3 only: fewer layers than the 94 of the config, for trying the path on fewer GPUs (the "
                         "line then names the layer count; not the config's number)")
@@ -313,8 +318,132 @@ def run_reference(a):
     return 0
 
 
+HOST_WORKLOADS = ("c1-host", "llama3-70b-host")
+
+
+def host_reference_case(name):
+    """The reference's host-mode case for a host workload: (desc JSON, tiers, budget, options, unit bytes, sample text).
+    C1 runs whole; C3 is sampled on 8 layers of the same 1.71 GB blobs (3 resident, 5 streamed through the 2-slot
+    ring): the reference's CPU backend keeps its "device" copies in host RAM too, and all 80 layers would not fit."""
+    from tierstream_b200 import abi, harness, host_bench, synth
+    w = host_bench.WORKLOADS[name]
+    if name == "c1-host":
+        m = host_bench.model_of(name)
+        m.write()
+        tiers = host_bench.tiers_of(name)
+        what = "C1 whole"
+    else:
+        m = synth.Model(os.path.join(harness.model_dir(), "tsb-bench-llama3-ref-sample.bin"), 8, 1, w["parts"],
+                        seed=w["seed"], top_k=1)
+        m.create_sparse()
+        tiers = [abi.SS_TIER_RESIDENT] * 3 + [abi.SS_TIER_PINNED] * 5
+        what = "8 layers of C3's 1.71 GB blobs (3 resident, 5 streamed per token through the 2-slot ring)"
+    b, o = host_bench.budget_options(name, m)
+    if name != "c1-host":
+        b.device_bytes = (3 + w["ring"] + 4) * m.unit_bytes + (1 << 30)
+    return host_bench.desc_of(name, m), tiers, b, o, m.unit_bytes, what
+
+
+def host_reference_measure(name, trace, warmup, steps, threads):
+    """The reference's host forward mode on its CPU backend (oracle/_ref, synchronous memcpy copies on its reader
+    threads) over warmup + steps forwards of the trace, less a run of the warm-up forwards alone: (GB/s streamed,
+    seconds of the timed forwards, sample text)."""
+    import oracle
+    desc_json, tiers, b, o, unit, what = host_reference_case(name)
+    o.reader_threads = threads
+    layers = json.loads(desc_json)["layers"]
+    all_layers = [1 if lay["kind"] == "blob" else 0 for lay in layers]
+    tr = trace[:, :len(layers)]
+
+    def timed(n):
+        t0 = time.perf_counter()
+        _, st = oracle.ref_host_replay(desc_json, tiers, b, o, tr[:n], all_layers)
+        return float(st[:, :, 2].sum() + st[:, :, 3].sum()) * unit, time.perf_counter() - t0
+
+    moved, dt = timed(warmup + steps)
+    w_moved, w_dt = timed(warmup) if warmup else (0.0, 0.0)
+    moved, dt = moved - w_moved, max(dt - w_dt, 1e-9)
+    text = ("%s: %d forwards (after %d warm-up forwards, subtracted) through the reference's host forward mode on its CPU "
+            "backend (oracle/_ref: ss_open / ss_layer_routes or ss_layer_all / ss_acquire / ss_release / ss_end, "
+            "every copy a memcpy of the real bytes), reader_threads %d, %.1f s" % (what, steps, warmup, threads, dt))
+    return moved / dt / 1e9, dt, text
+
+
+def host_reference(a):
+    """--impl reference for a host workload: the reference CPU backend with every usable CPU (reader_threads up to 64)
+    and, in a child process pinned to one CPU, with one."""
+    if int(os.environ.get("RANK", "0")) != 0:
+        return 0
+    import oracle
+    from tierstream_b200 import host_bench
+    if not oracle.ref_available():
+        print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libtsref.so (the reference's sources "
+                                                              "compiled by oracle/Makefile) is not built"}))
+        return 0
+    cpus = sorted(os.sched_getaffinity(0))
+    threads = a.ref_threads or min(64, len(cpus))
+    if a.ref_threads:
+        os.sched_setaffinity(0, set(cpus[:a.ref_threads]))
+    w = host_bench.WORKLOADS[a.workload]
+    trace = host_bench.routes_of(a.workload, a.warmup + a.steps)
+    v, dt, text = host_reference_measure(a.workload, trace, a.warmup, a.steps, threads)
+    line = {"impl": "reference", "metric": w["metric"], "value": round(v, 3), "unit": "GB/s", "n_gpus": a.gpus,
+            "steps": a.steps, "warmup": a.warmup, "ms_per_step": round(dt * 1e3 / a.steps, 3),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u8", "data": "synthetic",
+            "config": {"workload": a.workload, "layers": w["layers"], "units_per_layer": w["units"],
+                       "parts": list(w["parts"]), "resident": w["resident"], "ring_slots": w["ring"]},
+            "cpu_baseline": {"value": round(v, 3), "unit": "GB/s", "cores": threads, "kind": "reference",
+                             "sample": text},
+            "e2e": {"value": round(v, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    if not a.ref_threads:  # the same with one CPU, in a child pinned to it
+        r = subprocess.run([sys.executable, os.path.abspath(__file__), "--impl", "reference", "--workload",
+                            a.workload, "--steps", str(a.steps), "--warmup", str(a.warmup), "--ref-threads", "1"],
+                           capture_output=True, text=True)
+        one = [json.loads(x) for x in r.stdout.splitlines() if x.startswith("{")]
+        line["one_core"] = {"value": one[0]["value"], "sample": one[0]["cpu_baseline"]["sample"]} if one and \
+            "value" in one[0] else {"error": (r.stderr or r.stdout)[-300:]}
+    print(json.dumps(line))
+    return 0
+
+
+def host_main(a):
+    """A host workload's GPU leg (tierstream_b200/host_bench.py) with the roofline against this run's host-link copy
+    rate and, after the context closed, the reference's CPU backend on the same trace as the cpu_baseline."""
+    if int(os.environ.get("WORLD_SIZE", "1")) > 1:
+        raise SystemExit("the host-mode workloads run on one GPU")
+    import torch
+    from tierstream_b200 import host_bench
+    torch.cuda.set_device(0)
+    peak = h2d_peak(torch)
+    line, trace, bad = host_bench.run(a.workload, a.steps, a.warmup, torch, Clocks, 0)
+    line["roofline"] = {
+        "bound": "link", "kernel": "the forward's stream (pinned -> ring and slot copies, the readers behind them)",
+        "achieved": line["value"], "peak": round(peak, 3) if peak else None, "unit": "GB/s",
+        "frac": round(line["value"] / peak, 4) if peak else None, "traffic": None,
+        "peak_source": "measured in this run: copy-engine pinned->HBM 1 GiB, best of 5 (MEASURED_PEAKS.json has no "
+                       "host-link figure)",
+        "note": "achieved over the whole forward (the copies are not timed apart from the routes, acquires and readers "
+                "in host mode)"}
+    if not a.no_cpu_baseline:
+        cpus = sorted(os.sched_getaffinity(0))
+        threads = min(64, len(cpus))
+        v, _, text = host_reference_measure(a.workload, trace, a.warmup, a.steps, threads)
+        line["cpu_baseline"] = {"value": round(v, 3), "unit": "GB/s", "cores": threads, "kind": "reference",
+                                "sample": text}
+    print(json.dumps(line))
+    return 1 if bad else 0
+
+
 def main():
     a = args_()
+    if a.workload in HOST_WORKLOADS:
+        from tierstream_b200 import host_bench
+        w = host_bench.WORKLOADS[a.workload]
+        a.steps = a.steps if a.steps is not None else w["steps"]
+        a.warmup = a.warmup if a.warmup is not None else w["warmup"]
+        return host_reference(a) if a.impl == "reference" else host_main(a)
+    a.steps = a.steps if a.steps is not None else 64
+    a.warmup = a.warmup if a.warmup is not None else 8
     configure(a)
     if not a.spare:
         a.spare = SPARE
@@ -358,14 +487,18 @@ def main():
     barrier()
     peak = h2d_peak(torch) if rank == 0 and not a.peer else None
     read_peak = file_read_peak(model_path(), 3 * PART) if a.file else None
-    ids = synth.zipf_trace(a.warmup + a.steps, LAYERS, UNITS, TOP_K, s=ZIPF, seed=1 + rank)
+    # one trace per rank: warm-up, the device-timed steps, then one untimed and `steps` timed steps of the e2e leg (a
+    # second window of the same routing distribution)
+    full = synth.zipf_trace(a.warmup + 2 * a.steps + 1, LAYERS, UNITS, TOP_K, s=ZIPF, seed=1 + rank)
+    ids = full[:a.warmup + a.steps]
+    ids2_warm, ids2 = full[a.warmup + a.steps], full[a.warmup + a.steps + 1:]
     inclusive = 0 if a.peer else inclusive_of(a)
     t_open = time.perf_counter()
     setup = None
     if a.peer:
         from tierstream_b200 import peer as peer_mod, runtime
         # the planner's input: this rank's routing counts over a calibration window of its own trace distribution
-        cal = synth.zipf_trace(64, LAYERS, UNITS, TOP_K, s=ZIPF, seed=1001 + rank)
+        cal = synth.zipf_trace(64, LAYERS, UNITS, TOP_K, s=ZIPF, seed=1001 + rank, perm_seed=1 + rank)
         counts = np.bincount((np.arange(LAYERS)[None, :, None] * UNITS + cal).reshape(-1), minlength=LAYERS * UNITS)
         filler = None
         if qwen:
@@ -399,7 +532,6 @@ def main():
     unit = model.unit_bytes
     # the e2e leg's trace, and every routed unit's expected reader sums in both legs' modes, from the byte generator
     # on the device (outside the timed regions)
-    ids2 = synth.zipf_trace(a.steps, LAYERS, UNITS, TOP_K, s=ZIPF, seed=101 + rank)
     routed = np.unique(np.concatenate([(np.arange(LAYERS)[None, :, None] * UNITS + x).reshape(-1)
                                        for x in (ids[a.warmup:], ids2)]))
     t_exp = time.perf_counter()
@@ -458,7 +590,7 @@ def main():
         # (2) end to end: the same steps of a second trace window through the ABI with host buffers, the readers
         # computing the positional checksum (the reference GPU tests' check)
         # one untimed step through the e2e path first (its graph's first launch, host buffers), on a token of its own
-        run.step(synth.zipf_trace(1, LAYERS, UNITS, TOP_K, s=ZIPF, seed=201 + rank)[0], mode=0)
+        run.step(ids2_warm, mode=0)
         s2 = run.ctx.stats()
         outs2 = np.zeros((a.steps, LAYERS, TOP_K), dtype=np.uint64)
         step_ms = []

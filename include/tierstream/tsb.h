@@ -153,6 +153,12 @@ SS_API ss_status tsb_test_dg_corrupt(ss_ctx* c, int layer, int unit, uint64_t of
  * (-1 for no entry). n must be the layer's units. */
 SS_API ss_status tsb_test_host_locs(ss_ctx* c, int layer, int32_t* out, int n);
 
+/* Host forward mode, between forwards (test and benchmark hook): where unit (layer, unit)'s bytes are kept -
+ * *pinned its pinned host block (mapped: kernels can write it at the same address), *device its persistent device
+ * slot when it is resident; NULL for either it does not have. A benchmark whose model file is too large for the disk
+ * opens on a sparse file and writes every kept unit's bytes here from its generator before the first forward. */
+SS_API ss_status tsb_test_host_unit(ss_ctx* c, int layer, int unit, void** pinned, void** device);
+
 /* Test hook: [offset, offset + bytes) of the file at `path` into dst in pieces of `piece` bytes read by a pool of
  * `threads` reader threads (the file tier's reads), unbuffered (O_DIRECT, straight into dst when aligned) when direct
  * is set and the file system allows it. */

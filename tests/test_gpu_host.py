@@ -317,3 +317,30 @@ def test_layer_prefetch_overlaps_the_blob_stream(orc, ref):
     finally:
         ctx.close()
 
+
+
+class _NoClocks:
+    def __init__(self, index):
+        pass
+
+    def stop(self):
+        return {}
+
+
+@pytest.mark.parametrize("name", ["c1-host", "blob-sparse"])
+def test_host_bench_forwards_read_the_generator_bytes(monkeypatch, name):
+    """bench.py's host-mode leg (tierstream_b200/host_bench.py) at small size: forwards of tse_host_forward (routes,
+    acquire, reader through the device table, release, end - the engine loop in native code) over C1, and over a
+    sparse 6-layer blob model (1 MiB + 48 byte blobs, 2 resident, 2-slot ring) whose residents' slots and pinned blocks
+    are written from the generator after the open, as the Llama-3-70B-shaped workload does at full size. Every reader's
+    checksum equals the generator's, in both checksum modes."""
+    from tierstream_b200 import host_bench
+    if name == "blob-sparse":
+        monkeypatch.setitem(host_bench.WORKLOADS, name, dict(host_bench.WORKLOADS["llama3-70b-host"], layers=6,
+                                                             parts=((1 << 20) + 48,), resident=2, slices=64,
+                                                             file="tsb-test-blob-sparse.bin"))
+    line, trace, bad = host_bench.run(name, 4, 2, torch, _NoClocks, 0)
+    assert bad == 0
+    assert line["verified"]["units"] > 0 and line["value"] > 0 and line["streamed_units_per_token"] > 0
+    if name == "blob-sparse":
+        assert line["streamed_units_per_token"] == 4  # the 4 pinned layers, every forward

@@ -275,6 +275,7 @@ _PROTOS = {
     "tsb_test_dg_corrupt": (C.c_int, [vp, C.c_int, C.c_int, u64]),
     "tsb_xxh64": (u64, [vp, C.c_size_t, u64]),
     "tsb_test_host_locs": (C.c_int, [vp, C.c_int, P(i32), C.c_int]),
+    "tsb_test_host_unit": (C.c_int, [vp, C.c_int, C.c_int, P(vp), P(vp)]),
     "ss_layer_routes_dev": (C.c_int, [vp, C.c_int, vp, C.c_int, vp]),
     "tsb_cuda_arch": (C.c_int, []),
 }
@@ -287,6 +288,8 @@ _ENGINE_PROTOS = {
     "tse_fill_bytes": (None, [u64, u64, u64, vp, u32]),
     "tse_fill_units_device": (C.c_int, [u64, P(u64), u32, u64, vp, vp]),
     "tse_read_table": (C.c_int, [vp, vp, u32, u64, vp, u32, vp]),
+    "tse_read_table16": (C.c_int, [vp, vp, u32, u64, vp, u32, C.c_int, vp]),
+    "tse_host_forward": (C.c_int, [vp, vp, vp, u32, vp, vp, vp, u32, C.c_int, vp]),
     "tse_expect_sums": (C.c_int, [u64, vp, u32, u64, C.c_int, vp, u32, vp]),
 }
 

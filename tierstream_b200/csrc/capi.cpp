@@ -650,6 +650,11 @@ ss_status tsb_test_host_locs(ss_ctx* c, int layer, int32_t* out, int n) {
   return guard([&] { host_of(c, "tsb_test_host_locs").test_locs(layer, out, n); });
 }
 
+ss_status tsb_test_host_unit(ss_ctx* c, int layer, int unit, void** pinned, void** device) {
+  if (!c || !pinned || !device) return SS_E_INVALID;
+  return guard([&] { host_of(c, "tsb_test_host_unit").test_unit(layer, unit, pinned, device); });
+}
+
 // ---- peer tier (tsb.h) ----
 struct tsb_peer_store {
   std::unique_ptr<tsb::PeerStore> s;

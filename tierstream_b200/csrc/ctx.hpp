@@ -130,6 +130,9 @@ class HostContext {
   // between ss_acquire and ss_release of `layer`: per unit (loc, slot) of its table entry: (1, persistent slot),
   // (2, ring slot) or (0, -1) for no entry
   virtual void test_locs(int layer, int32_t* out, int n) const = 0;
+  // between forwards: where unit (layer, unit)'s bytes are kept - its pinned block (a mapped host address, usable by
+  // kernels) and its persistent device slot when resident; nullptr for either it does not have
+  virtual void test_unit(int layer, int unit, void** pinned, void** device) const = 0;
 };
 
 std::unique_ptr<HostContext> open_host_context(const Desc& d, const ss_budget& b, const Plan& p, const ss_options& o);

@@ -122,6 +122,50 @@ __global__ __launch_bounds__(kThreads) void table_reader_kernel(const uint64_t* 
   }
 }
 
+// Host forward mode's reader for units whose bytes are a multiple of 16 at 16-byte aligned addresses (every pinned
+// and device slot is): the same checksums as reader_kernel's modes, 16-byte loads, four in flight per thread.
+__global__ __launch_bounds__(kThreads) void table_reader16_kernel(const uint64_t* table, const int32_t* ids, uint32_t n,
+                                                                  uint64_t unit_bytes, unsigned long long* out,
+                                                                  int mode) {
+  const uint32_t i = blockIdx.x;
+  if (i >= n) return;
+  const uint4* base = reinterpret_cast<const uint4*>(table[ids[i]]);
+  uint64_t acc = 0;
+  if (base) {
+    const uint64_t n16 = unit_bytes / 16;
+    const uint64_t per = (n16 + gridDim.y - 1) / gridDim.y;
+    const uint64_t lo = per * blockIdx.y, hi = lo + per < n16 ? lo + per : n16;
+    constexpr uint32_t kStep = (16u * kThreads) % 251u;
+    uint64_t e = lo + threadIdx.x;
+    uint32_t m = uint32_t((e * 16) % 251);
+    for (; e + 3 * kThreads < hi; e += 4 * kThreads) {
+      uint4 w[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) w[k] = base[e + uint64_t(k) * kThreads];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        acc += group_sum(w[k], m, mode);
+        m += kStep;
+        if (m >= 251) m -= 251;
+      }
+    }
+    for (; e < hi; e += kThreads) {
+      acc += group_sum(base[e], m, mode);
+      m += kStep;
+      if (m >= 251) m -= 251;
+    }
+  }
+  __shared__ uint64_t part[kThreads / 32];
+  acc = warp_sum(acc);
+  if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = acc;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    uint64_t s = 0;
+    for (int k = 0; k < kThreads / 32; ++k) s += part[k];
+    atomicAdd(out + i, (unsigned long long)s);
+  }
+}
+
 #define CK(x)                                  \
   do {                                         \
     const cudaError_t e_ = (x);                \
@@ -330,6 +374,64 @@ __attribute__((visibility("default"))) int tse_read_table(const uint64_t* table_
   CK(cudaMemsetAsync(out_dev, 0, size_t(n) * 8, s));
   table_reader_kernel<<<dim3(n, slices), kThreads, 0, s>>>(table_dev, ids_dev, n, unit_bytes, out_dev);
   return int(cudaGetLastError());
+}
+
+// Host forward mode with 16-byte loads (unit_bytes a multiple of 16): mode 0 the positional checksum (as
+// tse_read_table), mode 1 the 32-bit word sum; on `stream`.
+__attribute__((visibility("default"))) int tse_read_table16(const uint64_t* table_dev, const int32_t* ids_dev,
+                                                            uint32_t n, uint64_t unit_bytes,
+                                                            unsigned long long* out_dev, uint32_t slices, int mode,
+                                                            void* stream) {
+  if (unit_bytes % 16 != 0 || (mode != 0 && mode != 1)) return int(cudaErrorInvalidValue);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  CK(cudaMemsetAsync(out_dev, 0, size_t(n) * 8, s));
+  table_reader16_kernel<<<dim3(n, slices ? slices : 1), kThreads, 0, s>>>(table_dev, ids_dev, n, unit_bytes, out_dev,
+                                                                          mode);
+  return int(cudaGetLastError());
+}
+
+// One host-mode forward of an engine over descriptor d, all of it native: ss_begin; per layer with units, its routes (ss_layer_routes
+// of routes[L][0..n_ids), or ss_layer_all when all_layers[L] != 0), ss_acquire on `stream`, the reader over the
+// layer's ids (the routed ids, or unit 0 for a whole layer) through the acquired device table, ss_release; ss_end.
+// ids_dev [layers][n_ids] (device) receives the token's ids by one copy from `routes` (pinned host memory for an
+// asynchronous copy) at the start; out_dev [layers][n_ids] the readers' checksums (mode 0 positional, 1 word sums;
+// 16-byte loads when unit_bytes % 16 == 0, else the byte reader, mode 0 only). Returns 0, a CUDA error, or
+// 1000 + an ss_status.
+__attribute__((visibility("default"))) int tse_host_forward(ss_ctx* c, const ss_desc* d, const int32_t* routes,
+                                                            uint32_t n_ids,
+                                                            const uint8_t* all_layers, int32_t* ids_dev,
+                                                            unsigned long long* out_dev, uint32_t slices, int mode,
+                                                            void* stream) {
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int layers = ss_desc_n_layers(d);
+  if (layers < 0) return 1000 + int(SS_E_INVALID);
+  CK(cudaMemcpyAsync(ids_dev, routes, sizeof(int32_t) * size_t(layers) * n_ids, cudaMemcpyHostToDevice, s));
+  CK(cudaMemsetAsync(out_dev, 0, sizeof(unsigned long long) * size_t(layers) * n_ids, s));
+  SS(ss_begin(c, nullptr, 0));
+  for (int L = 0; L < layers; ++L) {
+    const int units = ss_desc_layer_units(d, L);
+    if (units <= 0) continue;
+    const bool whole = all_layers && all_layers[L];
+    if (whole) SS(ss_layer_all(c, L));
+    else SS(ss_layer_routes(c, L, routes + size_t(L) * n_ids, int(n_ids)));
+    ss_layer_view v;
+    SS(ss_acquire(c, L, stream, &v));
+    const uint64_t unit_bytes = ss_desc_unit_bytes(d, L);
+    const uint32_t n = whole ? 1u : n_ids;
+    int32_t* ids = ids_dev + size_t(L) * n_ids;
+    unsigned long long* out = out_dev + size_t(L) * n_ids;
+    if (unit_bytes % 16 == 0) {
+      table_reader16_kernel<<<dim3(n, slices ? slices : 1), kThreads, 0, s>>>(v.table_dev, ids, n, unit_bytes, out,
+                                                                              mode);
+    } else {
+      if (mode != 0) return int(cudaErrorInvalidValue);
+      table_reader_kernel<<<dim3(n, slices ? slices : 1), kThreads, 0, s>>>(v.table_dev, ids, n, unit_bytes, out);
+    }
+    CK(cudaGetLastError());
+    SS(ss_release(c, L, stream));
+  }
+  SS(ss_end(c));
+  return 0;
 }
 
 // The reader alone (no capture): checksums of n units of gated layer g resolved through the context's table.

@@ -548,6 +548,17 @@ class HostCtx final : public HostContext {
     }
   }
 
+  void test_unit(int layer, int unit, void** pinned, void** device) const override {
+    check_layer(layer, "tsb_test_host_unit");
+    require(!in_fwd_, SS_E_INVALID, "tsb_test_host_unit: between forwards only");
+    const Lay& s = L_[size_t(layer)];
+    require(s.rs != nullptr && unit >= 0 && unit < d_.layers[size_t(layer)].n_units, SS_E_INVALID,
+            "tsb_test_host_unit: unit out of range");
+    *pinned = const_cast<char*>(pinned_of_[size_t(gidx(layer, unit))]);
+    const int slot = s.rs->slot(unit);
+    *device = slot < 0 ? nullptr : at(s.pool, uint64_t(slot) * stride(layer));
+  }
+
  private:
   enum Loc : int8_t { kNone = 0, kPersistent = 1, kRing = 2 };
   struct Ring {

@@ -219,6 +219,12 @@ class HostContext:
         abi.check(abi.load().tsb_test_host_locs(self.h, layer, out.ctypes.data_as(C.POINTER(C.c_int32)), n_units))
         return out.reshape(n_units, 2)
 
+    def unit_home(self, layer, unit):
+        """(pinned host block address or None, resident device slot address or None) of a unit, between forwards."""
+        p, d = C.c_void_p(), C.c_void_p()
+        abi.check(abi.load().tsb_test_host_unit(self.h, layer, unit, C.byref(p), C.byref(d)))
+        return p.value, d.value
+
     def layer_stats(self, layer):
         s = abi.ss_layer_stats()
         abi.check(abi.load().ss_stats_layer(self.h, layer, C.byref(s)))

@@ -127,10 +127,14 @@ class Model:
                            "layers": layers})
 
 
-def zipf_trace(tokens, layers, units, top_k, s=1.1, seed=1, rho=0.0, uniform=False):
-    """int32 [tokens][layers][top_k] routed ids (distinct within a row)."""
+def zipf_trace(tokens, layers, units, top_k, s=1.1, seed=1, rho=0.0, uniform=False, perm_seed=None):
+    """int32 [tokens][layers][top_k] routed ids (distinct within a row). perm_seed: the per-layer popularity
+    permutations from that seed instead of `seed` (another sample of the same routing distribution)."""
     rng = np.random.default_rng(seed)
     perms = [rng.permutation(units) for _ in range(layers)]
+    if perm_seed is not None:
+        prng = np.random.default_rng(perm_seed)
+        perms = [prng.permutation(units) for _ in range(layers)]
     if uniform:
         p = np.full(units, 1.0 / units)
     else:
