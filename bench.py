@@ -34,7 +34,7 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 LAYERS, UNITS, PART = 32, 8, 33030144
-TOP_K, ZIPF, RESIDENTS, SPARE = 2, 1.1, 102, 1
+TOP_K, ZIPF, RESIDENTS, SPARE, RHO = 2, 1.1, 102, 1, 0.0
 METRIC = "expert-miss stream GB/s (device-gated decode, Mixtral-8x7B-shaped MoE)"
 WORKLOAD, MODEL_FILE = "mixtral-8x7b-dg", "tsb-bench-mixtral-dg.bin"
 # BASELINE configs[4] (C5): 94 layers x 128 experts of 3 x 12,582,912 B (4096 x 1536 bf16), top-8 Zipf(1.2), one
@@ -45,6 +45,16 @@ WORKLOAD, MODEL_FILE = "mixtral-8x7b-dg", "tsb-bench-mixtral-dg.bin"
 QWEN3 = dict(LAYERS=94, UNITS=128, PART=12582912, TOP_K=8, ZIPF=1.2, RESIDENTS=94 * 8, SPARE=4,
              METRIC="expert-miss stream GB/s (device-gated decode, Qwen3-235B-A22B-shaped MoE, peer tier)",
              WORKLOAD="qwen3-235b-a22b-peer", MODEL_FILE="tsb-bench-qwen3-peer.bin")
+# BASELINE configs[3] (C4): 58 MoE layers x 256 routed experts of 3 x 14,680,064 B (7168 x 2048 fp8 e4m3 as random
+# bytes), top-8 Zipf(0.9) routes whose layers repeat their predecessor's experts with probability 0.5 (the config's
+# layer-to-layer correlation), exclusive tiers, 48 GB of VRAM per GPU for the gated slots (12 residents and 6 spare
+# slots per layer with the banks: 46.7 GB), each layer's routed ids predicting the next layer's on the device
+# (ss_dg_enqueue_predict from the export's own buffer). The 654 GB of experts live in the peer tier's stores (82 GB
+# per GPU at 8 GPUs; fewer GPUs take fewer layers with --layers), written on the device from the generator.
+DEEPSEEK = dict(LAYERS=58, UNITS=256, PART=14680064, TOP_K=8, ZIPF=0.9, RHO=0.5, RESIDENTS=58 * 12, SPARE=6,
+                METRIC="expert-miss stream GB/s (device-gated decode, DeepSeek-V3-shaped MoE, peer tier)",
+                WORKLOAD="deepseek-v3-peer", MODEL_FILE="tsb-bench-deepseek-peer.bin")
+DEVICE_FILLED = ("qwen3-235b-a22b-peer", "deepseek-v3-peer")  # sparse model files, stores written from the generator
 
 
 def args_():
@@ -81,15 +91,17 @@ def args_():
     p.add_argument("--round-every", type=int, default=0,
                    help="a placement round (ss_dg_round, defaults) after every N tokens, inside the timed steps")
     p.add_argument("--workload", default="mixtral-8x7b-dg",
-                   choices=["mixtral-8x7b-dg", "qwen3-235b-a22b-peer", "c1-host", "llama3-70b-host"],
+                   choices=["mixtral-8x7b-dg", "qwen3-235b-a22b-peer", "deepseek-v3-peer", "c1-host",
+                            "llama3-70b-host"],
                    help="mixtral-8x7b-dg: BASELINE configs[1] (default); qwen3-235b-a22b-peer: configs[4], the peer "
-                        "tier on 4 or more GPUs; c1-host and llama3-70b-host: configs[0] and [2] in the host forward "
+                        "tier on 4 or more GPUs; deepseek-v3-peer: configs[3], the peer tier on 8 GPUs (fewer with "
+                        "--layers); c1-host and llama3-70b-host: configs[0] and [2] in the host forward "
                         "mode on one GPU (tierstream_b200/host_bench.py)")
     p.add_argument("--ref-threads", type=int, default=0,
                    help="host workloads, --impl reference: the reference's reader_threads, pinned to that many CPUs "
                         "(0: every CPU this process may use, at most 64)")
     p.add_argument("--layers", type=int, default=0,
-                   help="qwen3 only: fewer layers than the 94 of the config, for trying the path on fewer GPUs (the "
+                   help="qwen3 / deepseek only: fewer layers than the config's, for fewer GPUs (the "
                         "line then names the layer count; not the config's number)")
     p.add_argument("--peer-copy", default="kernel", choices=["kernel", "ce"],
                    help="peer tier mover: the land kernel's SM loads or the copy engines")
@@ -110,13 +122,15 @@ def model_path():
 
 def configure(a):
     """Sets the workload's shape (the module constants)."""
-    if a.workload == "qwen3-235b-a22b-peer":
+    shapes = {"qwen3-235b-a22b-peer": (QWEN3, 8), "deepseek-v3-peer": (DEEPSEEK, 12)}
+    if a.workload in shapes:
+        shape, per_layer = shapes[a.workload]
         g = globals()
-        g.update(QWEN3)
+        g.update(shape)
         if a.layers:
             g["LAYERS"] = a.layers
-            g["RESIDENTS"] = a.layers * 8
-            g["MODEL_FILE"] = "tsb-bench-qwen3-peer-%d.bin" % a.layers
+            g["RESIDENTS"] = a.layers * per_layer
+            g["MODEL_FILE"] = shape["MODEL_FILE"].replace(".bin", "-%d.bin" % a.layers)
 
 
 class Clocks:
@@ -471,13 +485,13 @@ def main():
         if dist:
             dist.barrier()
 
-    qwen = a.workload == "qwen3-235b-a22b-peer"
+    qwen = a.workload in DEVICE_FILLED
     # descriptor hashes (the stores' and the landings' checks on the device) for every model written to disk; the
     # Qwen3-shaped stores are written on the device from the generator and checked by the readers' sums instead
     hashed = not qwen
     model = synth.Model(model_path(), LAYERS, UNITS, [PART] * 3, seed=0, top_k=TOP_K, with_hash=hashed)
     if qwen and not a.peer:
-        raise SystemExit("qwen3-235b-a22b-peer runs the peer tier only (its experts do not fit pinned RAM)")
+        raise SystemExit("%s runs the peer tier only (its experts do not fit pinned RAM)" % a.workload)
     if rank == 0:
         if qwen:
             model.create_sparse()
@@ -489,7 +503,7 @@ def main():
     read_peak = file_read_peak(model_path(), 3 * PART) if a.file else None
     # one trace per rank: warm-up, the device-timed steps, then one untimed and `steps` timed steps of the e2e leg (a
     # second window of the same routing distribution)
-    full = synth.zipf_trace(a.warmup + 2 * a.steps + 1, LAYERS, UNITS, TOP_K, s=ZIPF, seed=1 + rank)
+    full = synth.zipf_trace(a.warmup + 2 * a.steps + 1, LAYERS, UNITS, TOP_K, s=ZIPF, seed=1 + rank, rho=RHO)
     ids = full[:a.warmup + a.steps]
     ids2_warm, ids2 = full[a.warmup + a.steps], full[a.warmup + a.steps + 1:]
     inclusive = 0 if a.peer else inclusive_of(a)
@@ -498,7 +512,7 @@ def main():
     if a.peer:
         from tierstream_b200 import peer as peer_mod, runtime
         # the planner's input: this rank's routing counts over a calibration window of its own trace distribution
-        cal = synth.zipf_trace(64, LAYERS, UNITS, TOP_K, s=ZIPF, seed=1001 + rank, perm_seed=1 + rank)
+        cal = synth.zipf_trace(64, LAYERS, UNITS, TOP_K, s=ZIPF, seed=1001 + rank, perm_seed=1 + rank, rho=RHO)
         counts = np.bincount((np.arange(LAYERS)[None, :, None] * UNITS + cal).reshape(-1), minlength=LAYERS * UNITS)
         filler = None
         if qwen:
@@ -527,7 +541,8 @@ def main():
                         verify=hashed,
                         inclusive=inclusive, peer=setup.tier if setup else None,
                         disk_keys=disk_keys(a, resident_keys(1)) if a.file else (), disk_staging=a.staging,
-                        disk_queue=a.disk_queue, policy={"lru": 0, "scored": 1, "scored_auto": 2}[a.policy])
+                        disk_queue=a.disk_queue, policy={"lru": 0, "scored": 1, "scored_auto": 2}[a.policy],
+                        predict_prev=RHO > 0)
     t_open = time.perf_counter() - t_open
     unit = model.unit_bytes
     # the e2e leg's trace, and every routed unit's expected reader sums in both legs' modes, from the byte generator
@@ -613,7 +628,8 @@ def main():
         e2e_s = w1 - w0
         misses = s1["misses"] - s0["misses"]
         lookups = s1["lookups"] - s0["lookups"]
-        dg = {k: s1[k] - s0[k] for k in ("fetched", "prefetched", "bank_serves", "evicted", "evict_short",
+        dg = {k: s1[k] - s0[k] for k in ("fetched", "prefetched", "prefetch_used", "predicted", "predicted_true",
+                                         "bank_serves", "evicted", "evict_short",
                                          "writebacks_done", "collected_mid", "wb_forced", "wb_forced_wait_ns",
                                          "wb_boundary_flushed", "wb_deferred", "wb_cancelled", "resurrected",
                                          "wb_issued_bytes", "covered", "disk_reads", "disk_read_bytes",
@@ -657,7 +673,8 @@ def main():
         "warmup": a.warmup, "ms_per_step": round(dev_ms_max / a.steps, 3), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "u8", "data": "synthetic (seeded random bytes and Zipf routes)",
         "config": {"workload": WORKLOAD, "layers": LAYERS, "experts": UNITS, "part_bytes": PART,
-                   "unit_bytes": unit, "top_k": TOP_K, "zipf": ZIPF, "residents": RESIDENTS,
+                   "unit_bytes": unit, "top_k": TOP_K, "zipf": ZIPF, "rho": RHO, "residents": RESIDENTS,
+                   "predictions": "each layer's routed ids, for the next layer" if RHO > 0 else "none",
                    "spare_slots_per_layer": a.spare, "parallelism": "replicas" if world > 1 else "single",
                    "copy_mode": a.copy_mode,
                    "l2": "inputs larger than L2 (%.0f MB units, %.1f GB arena)" % (

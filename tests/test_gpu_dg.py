@@ -280,6 +280,34 @@ def test_predictions_tables_match_reference(small_model, orc, ref, monkeypatch, 
         run.close()
 
 
+def test_predictions_from_the_previous_layer_match_reference(small_model, orc, ref, monkeypatch):
+    """predict_prev: each layer's exported id buffer is also ss_dg_enqueue_predict's input for the next layer (read on
+    the device, no host predictions), on a trace whose layers repeat their predecessor's experts with probability 0.5
+    (BASELINE configs[3]'s correlation). Tables after every token equal the reference's replay given the same ids as
+    predictions; every reader's bytes are right; some prefetches are used."""
+    monkeypatch.setenv("TSB_DG_DETERMINISTIC", "1")
+    m = small_model
+    ids = synth.zipf_trace(30, m.layers, m.units, 2, s=0.9, seed=31, rho=0.5)
+    run = harness.DgRun(m, residents_per_layer=3, max_ids=2, predict_prev=True)
+    try:
+        P = m.layers * m.units - len(run.resident_keys)
+        cfg = runtime.replay_config([m.units] * m.layers, list(m.part_bytes),
+                                    persistent_slots=len(run.resident_keys) + m.layers, bank_slots=2,
+                                    blocks=P + m.layers, spare_target=m.layers, order=run.resident_keys,
+                                    tokens=ids.shape[0], n_ids=2, n_pred=2)
+        t_ref, s_ref = oracle.ref_replay(cfg, ids, ids)
+        want = expected_sums(m, orc)
+        for t in range(ids.shape[0]):
+            got = run.step(ids[t])
+            keys = np.arange(m.layers)[:, None] * m.units + ids[t]
+            assert np.array_equal(got, want[keys]), "token %d read wrong bytes" % t
+            assert np.array_equal(run.ctx.table(run.keys), t_ref[t]), "slot table differs after token %d" % t
+        st = run.ctx.stats()
+        assert st["prefetched"] == s_ref[-1][5] and st["prefetched"] > 0 and st["prefetch_used"] > 0
+    finally:
+        run.close()
+
+
 def file_tier_run(m, R=3, pinned=4, S=3, **kw):
     """A DgRun with the file tier: per layer units [0, R) resident, [R, R + pinned) pinned, the rest in the model file
     only (tier DISK)."""

@@ -51,11 +51,17 @@ def expected(m, orc):
     return out
 
 
-@pytest.mark.parametrize("dynamic,pin_planned", [(0, 1), (2, 0), (3, 1)])
-def test_c1_tables_counters_and_bytes_match_reference(c1_model, orc, ref, dynamic, pin_planned):
+@pytest.mark.parametrize("dynamic,pin_planned,scored", [(0, 1, 0), (2, 0, 0), (3, 1, 0), (2, 1, 1), (0, 1, 1)])
+def test_c1_tables_counters_and_bytes_match_reference(c1_model, orc, ref, dynamic, pin_planned, scored):
+    """scored: the resident set's SCORED policy (src/resident_set.cpp) with its default window, on Zipf routes so the
+    scores differ from recency; the reference's host mode runs the same options."""
     m = c1_model
     tiers, b, o = setup(m, dynamic, pin_planned)
-    routes = synth.zipf_trace(64, m.layers, m.units, 2, seed=1, uniform=True)
+    if scored:
+        o.policy = abi.SS_POLICY_SCORED
+        routes = synth.zipf_trace(64, m.layers, m.units, 2, s=1.0, seed=3)
+    else:
+        routes = synth.zipf_trace(64, m.layers, m.units, 2, seed=1, uniform=True)
     desc_json = m.desc(order="ranked")
     ref_locs, ref_stats = oracle.ref_host_replay(desc_json, tiers, b, o, routes, [0] * m.layers)
     desc = runtime.Desc(desc_json)

@@ -76,9 +76,17 @@ class DgSetup:
 
 
 class DgRun:
-    def __init__(self, model, n_pred=0, slices=64, mode=0, with_reader=True, peer=None, max_ids=2, **setup):
+    """A device-gated context and its engine stand-in's token graph. predict_prev: each layer's routed ids are also
+    its prediction of the next layer's (ss_dg_enqueue_predict reads the export's own id buffer on the device: the
+    predictor of traces whose layers repeat their predecessor's experts); n_pred > 0 instead predicts from ids the host
+    gives each step."""
+
+    def __init__(self, model, n_pred=0, slices=64, mode=0, with_reader=True, peer=None, max_ids=2, predict_prev=False,
+                 **setup):
         self.model = model
         G, U = model.layers, model.units
+        if predict_prev:
+            n_pred = max_ids
         self.G, self.U, self.n_ids, self.n_pred = G, U, max_ids, n_pred
         s = DgSetup(model, max_ids=max_ids, **setup)
         self.setup = s
@@ -94,14 +102,13 @@ class DgRun:
         self.out_dev = torch.zeros(G * max_ids, dtype=torch.int64, device="cuda")
         self.out_pin = torch.zeros(G * max_ids, dtype=torch.int64).pin_memory()
         self.stream.wait_stream(torch.cuda.current_stream())  # the zero fills above ran on torch's stream
+        pred_ptr = (self.ids_dev if predict_prev else self.pred_dev).data_ptr() if n_pred else 0
         self.graph = runtime.TokenGraph(self.ctx, G, self.ids_dev.data_ptr(), max_ids, self.out_dev.data_ptr(),
-                                        self.stream.cuda_stream, slices=slices, mode=mode,
-                                        pred_dev=self.pred_dev.data_ptr() if n_pred else 0, n_pred=n_pred,
-                                        with_reader=with_reader)
+                                        self.stream.cuda_stream, slices=slices, mode=mode, pred_dev=pred_ptr,
+                                        n_pred=n_pred, with_reader=with_reader)
         self.keys = G * U
         self.graphs = {mode: self.graph}
-        self._graph_args = dict(slices=slices, pred_dev=self.pred_dev.data_ptr() if n_pred else 0, n_pred=n_pred,
-                                with_reader=with_reader)
+        self._graph_args = dict(slices=slices, pred_dev=pred_ptr, n_pred=n_pred, with_reader=with_reader)
 
     def graph_for(self, mode):
         """The token graph whose readers check in `mode` (0: positional checksum, 1: word sum), captured on first use
