@@ -37,7 +37,10 @@ SS_API int tsb_move_timeouts(void);
  * Unit i is n_spans[i] (1..4) spans spans[4 i + s] of span_bytes[4 i + s] bytes hashed back to back (a gated unit's
  * parts). units_dev: device scratch of n x 72 bytes (the unit table is staged there); out_dev: n hashes (device);
  * expect_dev (may be NULL): n expected hashes, mismatches counted into *mismatches_dev (device word, not cleared).
- * Bit-exact with the reference's host xxh64 (xxh64.cpp:39-112). */
+ * Bit-exact with the reference's host xxh64 (xxh64.cpp:39-112). Returns after the kernel finished; SS_E_BACKEND when a
+ * staging copy inside the kernel did not complete in 2 s. That check reads and clears one word per device shared with
+ * tsb_xxh64_units_static: a call that overlaps another on the same device may report the other's timeout (the
+ * library's own verifications use words of their own). */
 SS_API ss_status tsb_xxh64_units(const void* const* spans, const uint64_t* span_bytes, const uint32_t* n_spans,
                                  uint32_t n, void* units_dev, const uint64_t* expect_dev, uint64_t* out_dev,
                                  uint32_t* mismatches_dev, void* stream);
@@ -47,7 +50,7 @@ SS_API ss_status tsb_xxh64_units(const void* const* spans, const uint64_t* span_
  * instead of caller memory: for callers that cannot allocate device memory. n above the maximum returns SS_E_INVALID.
  * The first call on a device looks the array up (make it before any stream capture on that device). The table needs
  * no zeroing; *mismatches_dev is added to, not cleared. One table per device: overlapping calls on a device race.
- * Returns after the kernel finished. */
+ * Returns after the kernel finished; its timeout report shares a word with tsb_xxh64_units (above). */
 #define TSB_XXH64_STATIC_MAX_UNITS 4096u
 SS_API ss_status tsb_xxh64_units_static(const void* const* spans, const uint64_t* span_bytes, const uint32_t* n_spans,
                                         uint32_t n, const uint64_t* expect_dev, uint64_t* out_dev,

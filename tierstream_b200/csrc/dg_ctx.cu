@@ -1228,7 +1228,7 @@ class CudaDgContext final : public DgContext {
     const bool in_slot = slot >= 0 && core_->home(key) != SlotCache::Home::Host && core_->home(key) != SlotCache::Home::File;
     if (!in_slot && (block < 0 || owned)) return;
     std::vector<char> bytes(size_t(x_.unit_bytes));
-    read_checked(layer, unit, bytes.data(), readers_ != nullptr);
+    read_checked(layer, unit, bytes.data(), readers_.get());
     if (in_slot)
       for (size_t p = 0; p < x_.part_bytes.size(); ++p)
         ck(cudaMemcpy(unit_part_dst(slot, uint32_t(p)), bytes.data() + x_.part_offset[p], size_t(x_.part_bytes[p]),
@@ -1763,7 +1763,7 @@ class CudaDgContext final : public DgContext {
   // A file-tier read: the unit's parts in pieces of at most 8 MiB, read by the reader pool at once (the reference
   // reads a unit in one pass on one reader); with verify_hash and descriptor hashes, the bytes are checked on the host
   // before any copy reads them (the reference's read_checked, dg_ctx.cpp:1625-1633).
-  void read_checked(int layer, int unit, char* dst, bool pooled = true) const {
+  void read_checked(int layer, int unit, char* dst, ReadPool* pool) const {
     const Layer& l = d_.layers[size_t(layer)];
     struct Piece {
       const SourceFile* f;
@@ -1778,9 +1778,9 @@ class CudaDgContext final : public DgContext {
         pieces.push_back({files_[size_t(p.source)].get(), base + o, std::min(kReadPiece, p.bytes - o), dst + at + o});
       at += p.bytes;
     }
-    if (pooled) {
-      readers_->run(pieces.size(), [&](size_t i) { pieces[i].f->read(pieces[i].dst, pieces[i].off, pieces[i].bytes); });
-    } else {  // (a read in flight: on its own reader thread, piece after piece)
+    if (pool) {
+      pool->run(pieces.size(), [&](size_t i) { pieces[i].f->read(pieces[i].dst, pieces[i].off, pieces[i].bytes); });
+    } else {
       for (const Piece& q : pieces) q.f->read(q.dst, q.off, q.bytes);
     }
     if (o_.verify_hash && !l.hash.empty())
@@ -1975,13 +1975,15 @@ class CudaDgContext final : public DgContext {
       mover_->set_reader([this](uint32_t key, char* dst) {
         const uint32_t g = uint32_t(std::upper_bound(x_.unit_base.begin(), x_.unit_base.end(), key) -
                                     x_.unit_base.begin()) - 1;
-        read_checked(x_.gated[g], int(key - x_.unit_base[g]), dst);
+        read_checked(x_.gated[g], int(key - x_.unit_base[g]), dst, readers_.get());
       });
-      if (x_.disk_queue > 1) {  // reads in flight: one reader thread per read the queue holds
-        async_ = std::make_unique<AsyncReads>(x_.disk_queue, [this](uint32_t key, char* dst) {
+      if (x_.disk_queue > 1) {  // reads in flight: one reader thread per read the queue holds, each read's pieces
+        // spread over a pool of that thread's own (a miss read in flight is as fast as a synchronous one)
+        for (uint32_t i = 0; i < x_.disk_queue; ++i) flight_pools_.push_back(std::make_unique<ReadPool>(n));
+        async_ = std::make_unique<AsyncReads>(x_.disk_queue, [this](uint32_t key, char* dst, unsigned worker) {
           const uint32_t g = uint32_t(std::upper_bound(x_.unit_base.begin(), x_.unit_base.end(), key) -
                                       x_.unit_base.begin()) - 1;
-          read_checked(x_.gated[g], int(key - x_.unit_base[g]), dst, false);
+          read_checked(x_.gated[g], int(key - x_.unit_base[g]), dst, flight_pools_[worker].get());
         });
         mover_->set_async(async_.get());
       }
@@ -2228,24 +2230,23 @@ class CudaDgContext final : public DgContext {
     auto* du = static_cast<dev::HashUnit*>(buf);
     auto* de = reinterpret_cast<uint64_t*>(du + n);
     auto* dout = de + n;
-    auto* dmis = reinterpret_cast<uint32_t*>(dout + n);
+    auto* dmis = reinterpret_cast<uint32_t*>(dout + n);  // [0] mismatches, [1] this call's staging timeouts
     cudaStream_t s = mover_->stream(Mover::kDem);
-    uint32_t mism = 0;
+    uint32_t words[2] = {0, 0};
     try {
       ck(cudaMemcpyAsync(du, units.data(), n * sizeof(dev::HashUnit), cudaMemcpyHostToDevice, s), "verify upload");
       ck(cudaMemcpyAsync(de, expect.data(), n * 8, cudaMemcpyHostToDevice, s), "verify upload");
-      ck(cudaMemsetAsync(dmis, 0, 4, s), "verify clear");
-      ck_launch(dev::launch_xxh64(du, uint32_t(n), de, dout, nullptr, dmis, s), "xxh64 kernel");
-      ck(cudaMemcpyAsync(&mism, dmis, 4, cudaMemcpyDeviceToHost, s), "verify result");
+      ck(cudaMemsetAsync(dmis, 0, 8, s), "verify clear");
+      ck_launch(dev::launch_xxh64(du, uint32_t(n), de, dout, nullptr, dmis, s, dmis + 1), "xxh64 kernel");
+      ck(cudaMemcpyAsync(words, dmis, 8, cudaMemcpyDeviceToHost, s), "verify result");
       ck(cudaStreamSynchronize(s), "verify sync");
-      uint32_t timeouts = 0;
-      ck(cudaError_t(dev::xxh64_take_timeouts(&timeouts)), "verify timeout word");
-      require(!timeouts, SS_E_BACKEND, "device-gated: a staging copy of the xxh64 kernel did not complete");
+      require(!words[1], SS_E_BACKEND, "device-gated: a staging copy of the xxh64 kernel did not complete");
     } catch (...) {
       cudaFree(buf);
       throw;
     }
     cudaFree(buf);
+    const uint32_t mism = words[0];
     require(mism == 0, SS_E_HASH,
             "device-gated: " + std::to_string(mism) + " resident unit(s) differ from their descriptor hashes");
   }
@@ -2261,6 +2262,7 @@ class CudaDgContext final : public DgContext {
     core_.reset();
     mover_.reset();
     async_.reset();
+    flight_pools_.clear();
     readers_.reset();
     for (char* a : bufs_.arena) cudaFree(a);
     if (bufs_.slot_of) cudaFree(bufs_.slot_of);
@@ -2282,6 +2284,7 @@ class CudaDgContext final : public DgContext {
   std::vector<std::unique_ptr<SourceFile>> files_;
   static constexpr uint64_t kReadPiece = uint64_t(8) << 20;  // file tier: the reader pool's piece
   std::unique_ptr<ReadPool> readers_;                        // file tier: the reads of one miss at once
+  std::vector<std::unique_ptr<ReadPool>> flight_pools_;      // file tier: one per reader thread of async_
   std::unique_ptr<AsyncReads> async_;                        // file tier: reads in flight (dg_disk_queue > 1)
   CudaMover::Buffers bufs_;
   uint32_t* ctl_ = nullptr;

@@ -173,10 +173,10 @@ PeerStore::PeerStore(const Desc& d, const std::vector<int32_t>& owner, int32_t r
         auto* du = static_cast<dev::HashUnit*>(buf);
         auto* de = reinterpret_cast<uint64_t*>(du + nb);
         auto* dout = de + nb;
-        auto* dmis = reinterpret_cast<uint32_t*>(dout + nb);
-        uint32_t mism = 0;
+        auto* dmis = reinterpret_cast<uint32_t*>(dout + nb);  // [0] mismatches, [1] this fill's staging timeouts
+        uint32_t words[2] = {0, 0};
         try {
-          ck(cudaMemsetAsync(dmis, 0, 4, s), "peer store verify clear");
+          ck(cudaMemsetAsync(dmis, 0, 8, s), "peer store verify clear");
           for (size_t first = 0; first < units_; first += chunk) {
             const size_t n = std::min(chunk, size_t(units_) - first);
             std::vector<dev::HashUnit> hu(n);
@@ -192,18 +192,17 @@ PeerStore::PeerStore(const Desc& d, const std::vector<int32_t>& owner, int32_t r
             }
             ck(cudaMemcpyAsync(du, hu.data(), n * sizeof(dev::HashUnit), cudaMemcpyHostToDevice, s), "verify upload");
             ck(cudaMemcpyAsync(de, want.data(), n * 8, cudaMemcpyHostToDevice, s), "verify upload");
-            ck(cudaError_t(dev::launch_xxh64(du, uint32_t(n), de, dout, nullptr, dmis, s)), "xxh64 kernel");
+            ck(cudaError_t(dev::launch_xxh64(du, uint32_t(n), de, dout, nullptr, dmis, s, dmis + 1)), "xxh64 kernel");
             ck(cudaStreamSynchronize(s), "peer store verify");  // the host tables are reused
           }
-          ck(cudaMemcpy(&mism, dmis, 4, cudaMemcpyDeviceToHost), "peer store verify result");
-          uint32_t timeouts = 0;
-          ck(cudaError_t(dev::xxh64_take_timeouts(&timeouts)), "peer store verify timeout word");
-          require(!timeouts, SS_E_BACKEND, "peer tier: a staging copy of the xxh64 kernel did not complete");
+          ck(cudaMemcpy(words, dmis, 8, cudaMemcpyDeviceToHost), "peer store verify result");
+          require(!words[1], SS_E_BACKEND, "peer tier: a staging copy of the xxh64 kernel did not complete");
         } catch (...) {
           cudaFree(buf);
           throw;
         }
         cudaFree(buf);
+        const uint32_t mism = words[0];
         require(mism == 0, SS_E_HASH,
                 "peer tier: " + std::to_string(mism) + " stored unit(s) differ from their descriptor hashes");
       }

@@ -108,8 +108,9 @@ void SourceFile::read(void* dst, uint64_t offset, uint64_t bytes) const {
   }
 }
 
-AsyncReads::AsyncReads(unsigned threads, std::function<void(uint32_t, char*)> read) : read_(std::move(read)) {
-  for (unsigned i = 0; i < std::max(1u, threads); ++i) th_.emplace_back([this] { loop(); });
+AsyncReads::AsyncReads(unsigned threads, std::function<void(uint32_t, char*, unsigned)> read)
+    : read_(std::move(read)) {
+  for (unsigned i = 0; i < std::max(1u, threads); ++i) th_.emplace_back([this, i] { loop(i); });
 }
 
 AsyncReads::~AsyncReads() {
@@ -151,7 +152,7 @@ uint64_t AsyncReads::end(void* h) {
   return j->ns;
 }
 
-void AsyncReads::loop() {
+void AsyncReads::loop(unsigned worker) {
   for (;;) {
     Job* j = nullptr;
     {
@@ -167,7 +168,7 @@ void AsyncReads::loop() {
     }
     const auto t0 = std::chrono::steady_clock::now();
     try {
-      read_(j->key, j->dst);
+      read_(j->key, j->dst, worker);
     } catch (...) {
       j->err = std::current_exception();
     }

@@ -23,7 +23,8 @@ namespace tsb {
 // at destruction.
 class AsyncReads {
  public:
-  AsyncReads(unsigned threads, std::function<void(uint32_t, char*)> read);
+  // read(key, dst, worker): runs on reader thread `worker` (0 .. threads - 1), one read per thread at a time
+  AsyncReads(unsigned threads, std::function<void(uint32_t, char*, unsigned)> read);
   ~AsyncReads();
   AsyncReads(const AsyncReads&) = delete;
   AsyncReads& operator=(const AsyncReads&) = delete;
@@ -39,8 +40,8 @@ class AsyncReads {
     std::exception_ptr err;
     uint64_t ns = 0;
   };
-  void loop();
-  std::function<void(uint32_t, char*)> read_;
+  void loop(unsigned worker);
+  std::function<void(uint32_t, char*, unsigned)> read_;
   std::mutex mu_;
   std::condition_variable cv_, done_cv_;
   std::vector<Job*> q_;                    // queued, oldest first (owned)

@@ -177,7 +177,7 @@ ss_status tsb_test_async_reads(const char* path, const uint64_t* offsets, uint32
     tsb::require(path && (offsets || !n) && (dst || !n) && threads >= 1 && threads <= 64, SS_E_INVALID,
                  "tsb_test_async_reads: bad argument");
     tsb::SourceFile f(path, 4096, true);
-    tsb::AsyncReads q(threads, [&](uint32_t i, char* out) { f.read(out, offsets[i], bytes); });
+    tsb::AsyncReads q(threads, [&](uint32_t i, char* out, unsigned) { f.read(out, offsets[i], bytes); });
     std::vector<void*> h(n);
     for (uint32_t i = 0; i < n; ++i) h[i] = q.begin(i, static_cast<char*>(dst) + uint64_t(i) * bytes);
     std::exception_ptr first;
