@@ -211,3 +211,42 @@ def test_move_kernel_refuses_unaligned():
     by = (C.c_uint64 * 1)(64)
     st = lib.tsb_move(sp, dp, by, 1, None, None, None, 0, None, 0, None, 0, None)
     assert st == abi.SS_E_INVALID and b"multiple of 16" in lib.ss_last_error()
+
+
+_DEVICE_CHILD = r"""
+import json, sys
+import numpy as np
+import torch
+sys.path.insert(0, sys.argv[1])
+sys.path.insert(0, sys.argv[1] + "/tests")
+from test_gpu_kernels import xxh_units
+out = {}
+for dev in (0, 1):  # device 0 first: device 1's first K3 launch comes after the library already ran on device 0
+    torch.cuda.set_device(dev)
+    h = np.random.default_rng(7).integers(0, 256, size=(3 << 20) + 40, dtype=np.uint8)
+    data = torch.from_numpy(h).cuda()
+    base = data.data_ptr()
+    units = [[(base, 1 << 20)], [(base + (1 << 20), 1 << 20), (base + (2 << 20), (1 << 20) + 40)]]
+    got, _ = xxh_units(units)
+    out[dev] = [int(x) for x in got]
+print(json.dumps(out))
+"""
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_xxh64_on_a_second_device_of_a_fresh_process(orc):
+    """K3's shared-memory attribute is set per device: a fresh process that hashes on device 0 and then, with nothing
+    of the library opened on device 1, on device 1 gets the oracle's hashes on both."""
+    import json
+    import os
+    import subprocess
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    r = subprocess.run([sys.executable, "-c", _DEVICE_CHILD, root], capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stderr[-2000:]
+    got = json.loads(r.stdout.strip().splitlines()[-1])
+    h = np.random.default_rng(7).integers(0, 256, size=(3 << 20) + 40, dtype=np.uint8)
+    a, b = h[:1 << 20], h[1 << 20:]
+    want = [orc.orc_xxh64(np.ascontiguousarray(a).ctypes.data, a.size, 0),
+            orc.orc_xxh64(np.ascontiguousarray(b).ctypes.data, b.size, 0)]
+    assert got["0"] == want and got["1"] == want
