@@ -57,7 +57,8 @@ struct Op {
   int32_t val = 0;
   Ev* ev = nullptr;
   uint64_t n = 0;
-  std::vector<int32_t> table;
+  std::vector<int32_t> table;  // (Table: the entries from table_first on)
+  uint32_t table_first = 0;
 };
 
 uint64_t checksum(const uint8_t* p, uint64_t n) {
@@ -254,6 +255,16 @@ class AsyncMover final : public Mover {
     enqueue(kDem, std::move(op));
     sync(kDem);
   }
+  void upload_table_ranges(const int32_t* t, const uint32_t* ranges, uint32_t n) override {
+    for (uint32_t i = 0; i < n; ++i) {
+      Op op;
+      op.kind = Op::Table;
+      op.table_first = ranges[2 * i];
+      op.table.assign(t + ranges[2 * i], t + ranges[2 * i] + ranges[2 * i + 1]);
+      enqueue(kDem, std::move(op));
+    }
+    sync(kDem);
+  }
   void sync_all() {
     for (int s = 0; s < 3; ++s) sync(Stream(s));
   }
@@ -315,7 +326,7 @@ class AsyncMover final : public Mover {
       switch (op.kind) {
         case Op::Write: *op.word = op.val; break;
         case Op::Record: op.ev->completed = std::max(op.ev->completed, op.n); break;
-        case Op::Table: std::copy(op.table.begin(), op.table.end(), dtab_.begin()); break;
+        case Op::Table: std::copy(op.table.begin(), op.table.end(), dtab_.begin() + op.table_first); break;
         default: break;
       }
       if (op.ref_block != INT_MIN) {
@@ -536,6 +547,7 @@ void dg_async_replay(const tsb_dg_replay_config* c, const int32_t* ids, const in
         held_keys[lg] = held_now;
         held[lg] = 1;
       }
+      core->set_range_uploads(std::any_of(held.begin(), held.end(), [](auto h) { return h != 0; }));
     }
     m.sync_all();
   } catch (...) {

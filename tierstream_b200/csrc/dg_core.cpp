@@ -44,6 +44,8 @@ SlotCache::SlotCache(const CacheConfig& cfg, Mover* m) : c_(cfg), m_(m) {
               " bank slots per bank (dg_max_ids), " + std::to_string(c_.bank_slots) + " configured");
   stage_ev_.assign(c_.disk_staging, nullptr);
   run_.assign(c_.n_units.size(), 1);
+  dirty_lo_.assign(c_.n_units.size(), kNil);
+  dirty_hi_.assign(c_.n_units.size(), 0);
   rs_.assign(keys_, 0.0);
   rhits_.assign(keys_, 0);
   if (c_.scored) {  // the history's tables exist from the open (the service thread never allocates)
@@ -132,7 +134,7 @@ void SlotCache::touch(uint32_t k) {
 void SlotCache::leave_device(uint32_t k) {
   if (recent_.has(k)) recent_.erase(k);
   --on_device_;
-  table_[k] = -1;
+  set_entry(k, -1);
 }
 
 void SlotCache::home_push(uint32_t k, bool cold) {
@@ -178,8 +180,51 @@ void* SlotCache::event() {
   return ev;
 }
 
-void SlotCache::publish(Mover::Stream s, uint32_t k, int32_t v) {
+void SlotCache::set_entry(uint32_t k, int32_t v) {
   table_[k] = v;
+  const uint32_t g = gated_of(k);
+  dirty_lo_[g] = std::min(dirty_lo_[g], k);
+  dirty_hi_[g] = std::max(dirty_hi_[g], k);
+}
+
+void SlotCache::clear_dirty() {
+  std::fill(dirty_lo_.begin(), dirty_lo_.end(), kNil);
+  std::fill(dirty_hi_.begin(), dirty_hi_.end(), 0u);
+}
+
+// The mirror to the device: whole, or (held layers) only each layer's changed range; the marks are cleared once the
+// mover took the upload (a failed one keeps them for the next).
+void SlotCache::upload() {
+  if (!ranged_) {
+    m_->upload_table(table_.data(), keys_);
+    clear_dirty();
+    device_table_known_ = false;
+    return;
+  }
+  ranges_.clear();
+  for (size_t g = 0; g < dirty_lo_.size(); ++g)
+    if (dirty_lo_[g] <= dirty_hi_[g]) {
+      ranges_.push_back(dirty_lo_[g]);
+      ranges_.push_back(dirty_hi_[g] - dirty_lo_[g] + 1);
+    }
+  m_->upload_table_ranges(table_.data(), ranges_.data(), uint32_t(ranges_.size() / 2));
+  if (!device_table_known_) {  // every change since the last whole upload was marked: the device now equals the mirror
+    device_table_ = table_;
+    device_table_known_ = true;
+  } else {
+    for (size_t r = 0; r < ranges_.size(); r += 2)
+      std::copy_n(table_.begin() + ranges_[r], ranges_[r + 1], device_table_.begin() + ranges_[r]);
+  }
+  clear_dirty();
+}
+
+void SlotCache::set_range_uploads(bool on) {
+  ranged_ = on;
+  if (!on) device_table_known_ = false;
+}
+
+void SlotCache::publish(Mover::Stream s, uint32_t k, int32_t v) {
+  set_entry(k, v);
   m_->publish(s, k, v);
 }
 
@@ -235,7 +280,7 @@ void SlotCache::place(const std::vector<uint32_t>& order, const std::vector<uint
   recent_.reset(keys_);
   for (uint32_t k = 0; k < keys_; ++k) {
     Entry& x = e_[k] = Entry{};
-    table_[k] = -1;
+    set_entry(k, -1);
     if (resident[k]) continue;
     if (c_.disk_tier && !gets_block[k]) {
       x.home = Home::File;
@@ -402,7 +447,7 @@ void SlotCache::undo_pending(const Pending& p) {
   Entry& x = e_[p.key];
   const uint32_t g = gated_of(p.key);
   if (p.bank) {
-    table_[p.key] = -1;
+    set_entry(p.key, -1);
     bank_key_[size_t(p.slot) - bank_first_] = kNil;
     banked_.erase(std::find(banked_.begin(), banked_.end(), p.key));
     --st_.bank_serves;
@@ -673,7 +718,7 @@ bool SlotCache::fetch(uint32_t g, uint32_t unit, bool prefetch) {
       }
       throw;
     }
-    table_[k] = slot;  // the mirror now; the device's entry with the copy
+    set_entry(k, slot);  // the mirror now; the device's entry with the copy
     --on_file_;
   } else {
     if (mut_ == kEntryBeforeCopy) publish(s, k, slot);  // test-only fault: the entry before its bytes
@@ -850,7 +895,7 @@ void SlotCache::end_token(const std::vector<uint32_t>& keep, uint32_t rows) {
     Entry& x = e_[k];
     if (x.home == Home::Bank) {
       to_lower(k);
-      table_[k] = -1;
+      set_entry(k, -1);
     }
     recycle(x.pf_done);
     x.via_pf = false;
@@ -940,7 +985,7 @@ void SlotCache::end_token(const std::vector<uint32_t>& keep, uint32_t rows) {
   // (4) the table, then the write-backs behind it: deferred ones carried by the larger of this and the last boundary's
   // evictions (the older ones flushed now), or issued at once on the write-back stream
   const size_t n_evict = victims_.size();
-  m_->upload_table(table_.data(), keys_);
+  upload();
   const size_t carry = std::max(n_evict, prev_evict_);
   const size_t n_flush = deferred_.size() > carry ? deferred_.size() - carry : 0;
   prev_evict_ = n_evict;
@@ -1223,7 +1268,7 @@ SlotCache::ResidentResult SlotCache::make_resident(uint32_t g, const std::vector
       m_->h2d(Mover::kDem, slot, src, k);
       publish(Mover::kDem, k, slot);
     } catch (...) {
-      table_[k] = -1;
+      set_entry(k, -1);
       free_slots_.give(slot);
       throw;
     }
@@ -1363,7 +1408,7 @@ SlotCache::ResidentResult SlotCache::make_resident(uint32_t g, const std::vector
     while (!reads.empty()) end_read(0);
     settle_writes();
     settle_copies();
-    m_->upload_table(table_.data(), keys_);  // (syncs the demand stream) every changed entry, the victims' -1 included
+    upload();  // (syncs the demand stream) every changed entry, the victims' -1 included
   } catch (...) {
     for (const Read& rd : reads) {  // reads not ended give their slots back (their keys never changed home)
       try {
@@ -1378,7 +1423,7 @@ SlotCache::ResidentResult SlotCache::make_resident(uint32_t g, const std::vector
       try {
         settle_writes();
         settle_copies();
-        m_->upload_table(table_.data(), keys_);
+        upload();
         uploaded = true;
       } catch (...) {
       }
@@ -1490,14 +1535,14 @@ RoundOut SlotCache::round(const RoundIn& in, const std::vector<uint32_t>& kept_k
       publish(Mover::kDem, k, slot);
       m_->sync(Mover::kDem);
     } catch (...) {
-      table_[k] = -1;
+      set_entry(k, -1);
       free_slots_.give(slot);
       throw;
     }
     spent += ub;
     out.bytes_h2d += ub;
     if (stop_asked()) {
-      table_[k] = -1;
+      set_entry(k, -1);
       free_slots_.give(slot);
       return false;
     }
@@ -1634,12 +1679,12 @@ RoundOut SlotCache::round(const RoundIn& in, const std::vector<uint32_t>& kept_k
       }
       while (!reads.empty()) commit_read();
     }
-    m_->upload_table(table_.data(), keys_);  // (syncs the demand stream) every changed entry
+    upload();  // (syncs the demand stream) every changed entry
   } catch (...) {
     for (const Landing& rd : reads) free_blocks_.give(rd.block);  // never committed: their units stay in their files
     reads.clear();
     try {  // the moves made so far go up (a failed device fails this too; the caller then poisons the context)
-      m_->upload_table(table_.data(), keys_);
+      upload();
     } catch (...) {
     }
     account();
@@ -1677,12 +1722,12 @@ uint32_t SlotCache::seed(const std::vector<uint32_t>& keys) {
     x.block = -1;
     x.slot = slot;
     x.home = Home::Device;
-    table_[k] = slot;
+    set_entry(k, slot);
     touch(k);
     ++on_device_;
     ++seeded;
   }
-  if (seeded) m_->upload_table(table_.data(), keys_);  // syncs kDem: the copies landed before their blocks are reused
+  if (seeded) upload();  // syncs kDem: the copies landed before their blocks are reused
   return seeded;
 }
 
@@ -1884,7 +1929,9 @@ void SlotCache::reset_open() {
   prev_evict_ = 0;
   credit_ = 0;
   outstanding_ = 0;
-  m_->upload_table(table_.data(), keys_);
+  m_->upload_table(table_.data(), keys_);  // the open's whole table
+  clear_dirty();
+  device_table_known_ = false;
 }
 
 // ---- invariants ----
@@ -1894,6 +1941,12 @@ void SlotCache::check() const {
     if (i < 0 || size_t(i) >= v.size() || v[size_t(i)]) broken(what);
     v[size_t(i)] = 1;
   };
+  if (ranged_ && device_table_known_)  // every entry the device does not hold yet is marked for the next upload
+    for (uint32_t k = 0; k < keys_; ++k)
+      if (table_[k] != device_table_[k]) {
+        const uint32_t g = gated_of(k);
+        if (k < dirty_lo_[g] || k > dirty_hi_[g]) broken("a table entry changed without its mark");
+      }
   uint32_t listed = 0, homes_listed = 0, dev = 0, hosts = 0, files = 0;
   for (uint32_t k = recent_.front(); k != kNil; k = recent_.older(k)) {
     if (++listed > keys_) broken("the recency list has a cycle");

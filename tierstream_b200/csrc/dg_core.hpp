@@ -91,6 +91,9 @@ class Mover {
   virtual void event_sync(void* ev) = 0;
   virtual void sync(Stream s) = 0;
   virtual void upload_table(const int32_t* table, uint32_t n) = 0;  // the whole table on kDem, then sync
+  // Only entries [ranges[2 i], ranges[2 i] + ranges[2 i + 1]) for i < n, on kDem, then sync (also with n = 0): the
+  // device table's other entries are not written.
+  virtual void upload_table_ranges(const int32_t* table, const uint32_t* ranges, uint32_t n) = 0;
   // Timing marks on kDem for a layer with a miss: which = 0 before its first demand copy, 1 after its ready.
   virtual void diag_mark(uint32_t g, int which) {
     (void)g;
@@ -281,6 +284,9 @@ class SlotCache {
   void set_pressure(uint32_t free_per_token, uint32_t evict_recent);
   void set_clean_evict(bool on);
   void set_pf_revert(bool on);
+  // While some layer is held (ss_dg_make_resident): uploads write only the entries changed since the last upload,
+  // so an engine kernel reading a held layer's entries never meets a write; off: the whole table in one copy.
+  void set_range_uploads(bool on);
   void set_mutation(int m) { mut_ = m; }
   // Every ownership rule (throws SS_E_BACKEND naming the first broken one).
   void check() const;
@@ -463,6 +469,15 @@ class SlotCache {
   uint32_t keys_ = 0, slots_ = 0, bank_first_ = 0;
   std::vector<Entry> e_;
   std::vector<int32_t> table_;
+  // Changed entries since the last upload: per gated layer the range [dirty_lo_, dirty_hi_] of keys written (empty
+  // while lo > hi). device_table_: the device's table as of the last range upload (while device_table_known_), which
+  // check() compares with the marks.
+  std::vector<uint32_t> dirty_lo_, dirty_hi_, ranges_;
+  std::vector<int32_t> device_table_;
+  bool ranged_ = false, device_table_known_ = false;
+  void set_entry(uint32_t k, int32_t v);
+  void clear_dirty();
+  void upload();
   LifoPool free_slots_, free_blocks_;
   KeyList recent_, homes_;  // homes_: the file tier's pinned homes, front = most recently homed
   uint32_t on_device_ = 0, backed_ = 0, on_file_ = 0;

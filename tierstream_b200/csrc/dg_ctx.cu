@@ -555,6 +555,23 @@ class CudaMover final : public Mover {
     ck(cudaMemcpyAsync(b_.slot_of, table_pin_, size_t(n) * 4, cudaMemcpyHostToDevice, s_[kDem]), "cudaMemcpyAsync (table)");
     ck(cudaStreamSynchronize(s_[kDem]), "cudaStreamSynchronize (table)");
   }
+  // Each range staged in the pinned mirror and copied on its own; the rest of the device table is never written. A
+  // copy that fails to enqueue lets those already enqueued finish first (they read the staging the retry refills).
+  void upload_table_ranges(const int32_t* t, const uint32_t* ranges, uint32_t n) override {
+    flush(kDem);
+    try {
+      for (uint32_t i = 0; i < n; ++i) {
+        const size_t first = ranges[2 * i], count = ranges[2 * i + 1];
+        std::memcpy(table_pin_ + first, t + first, count * 4);
+        ck(cudaMemcpyAsync(b_.slot_of + first, table_pin_ + first, count * 4, cudaMemcpyHostToDevice, s_[kDem]),
+           "cudaMemcpyAsync (table range)");
+      }
+    } catch (...) {
+      cudaStreamSynchronize(s_[kDem]);
+      throw;
+    }
+    ck(cudaStreamSynchronize(s_[kDem]), "cudaStreamSynchronize (table)");
+  }
   void drain_all() noexcept {
     for (cudaStream_t s : s_)
       if (s) cudaStreamSynchronize(s);
@@ -1335,6 +1352,7 @@ class CudaDgContext final : public DgContext {
     check_g(g, "ss_dg_keep");
     keep_[size_t(g)] = keys_of(g, ids, n, "ss_dg_keep", "unit");
     held_[size_t(g)] = 0;  // a plain keep: g is exported again
+    held_changed();
   }
   // ss_dg_make_resident: the units of gated layer g all on the device and kept there; g is not exported while held (the
   // engine reads its units through the table without an export); n = 0 releases it.
@@ -1345,12 +1363,14 @@ class CudaDgContext final : public DgContext {
     if (keys.empty()) {  // a release
       keep_[size_t(g)].clear();
       held_[size_t(g)] = 0;
+      held_changed();
       return;
     }
     std::vector<uint32_t> units(ids, ids + n);  // (checked: 0 <= id < units of g)
     core_->make_resident(uint32_t(g), units, keep_all());  // a refusal changes nothing (g keeps its former keep)
     keep_[size_t(g)] = std::move(keys);
     held_[size_t(g)] = 1;
+    held_changed();
   }
   uint32_t residency(ss_dg_unit* out, uint32_t cap) override {
     require(!in_token_, SS_E_INVALID, "ss_dg_residency: between tokens only");
@@ -1604,6 +1624,7 @@ class CudaDgContext final : public DgContext {
       core_->reset_open();
       for (auto& k : keep_) k.clear();
       std::fill(held_.begin(), held_.end(), uint8_t(0));
+      held_changed();
     } catch (...) {
       poisoned_ = true;
       throw;
@@ -1709,6 +1730,10 @@ class CudaDgContext final : public DgContext {
   }
   void check_g(int g, const char* fn) const {
     require(g >= 0 && size_t(g) < x_.gated.size(), SS_E_INVALID, std::string(fn) + ": gated layer out of range");
+  }
+  // A layer held or released: table uploads write only changed entries while any layer is held.
+  void held_changed() {
+    core_->set_range_uploads(std::any_of(held_.begin(), held_.end(), [](uint8_t h) { return h != 0; }));
   }
   // The keys of units `ids[0..n)` of gated layer g, each checked (`fn`: the entry point; `what`: "unit" or "id").
   std::vector<uint32_t> keys_of(int g, const int32_t* ids, int n, const char* fn, const char* what) const {

@@ -62,6 +62,10 @@ class HostMover final : public Mover {
   void event_sync(void*) override {}
   void sync(Stream) override {}
   void upload_table(const int32_t* t, uint32_t n) override { std::memcpy(table_.data(), t, size_t(n) * 4); }
+  void upload_table_ranges(const int32_t* t, const uint32_t* ranges, uint32_t n) override {
+    for (uint32_t i = 0; i < n; ++i)
+      std::memcpy(table_.data() + ranges[2 * i], t + ranges[2 * i], size_t(ranges[2 * i + 1]) * 4);
+  }
 
   std::vector<uint64_t> parts_;
   std::vector<int32_t> table_;
@@ -214,6 +218,7 @@ void dg_replay(const tsb_dg_replay_config* c, const int32_t* ids, const int32_t*
       held_keys[lg] = held_now;
       held[lg] = 1;
     }
+    core.set_range_uploads(std::any_of(held.begin(), held.end(), [](auto h) { return h != 0; }));
     if (c->rstats) std::memcpy(c->rstats + size_t(t) * 6, rsum, sizeof rsum);
     if (c->mstats) {
       const auto& q = core.stats();
