@@ -308,6 +308,55 @@ def test_predictions_from_the_previous_layer_match_reference(small_model, orc, r
         run.close()
 
 
+def test_held_layers_match_reference(small_model, orc, ref, monkeypatch):
+    """ss_dg_make_resident on the GPU: after chosen tokens a gated layer's units are made resident and held, and one is
+    released later. The engine's graph neither exports nor waits for a held layer (its reader resolves the held units
+    through ss_dg_slot). Tables after every token, the held-layer events applied, equal the reference's replay of the
+    same events; every reader's bytes are right; check() after every token proves that each table entry the device
+    does not hold yet is marked for the next upload (while a layer is held, uploads write only changed entries)."""
+    monkeypatch.setenv("TSB_DG_DETERMINISTIC", "1")
+    m = small_model
+    G, U, T = m.layers, m.units, 30
+    events = [(4, 2, (0, 5, 9)), (10, 4, (3, 7, 11)), (18, 2, ())]  # after that token: hold ids, () releases
+    active = {}
+    held_at = []
+    for t in range(T):
+        held_at.append(dict(active))
+        for te, g, u in events:
+            if te == t:
+                if u:
+                    active[g] = u
+                else:
+                    active.pop(g, None)
+    ids = synth.zipf_trace(T, G, U, 2, s=0.9, seed=51)
+    rng = np.random.default_rng(52)
+    for t in range(T):  # a held layer routes only to its held units
+        for g, u in held_at[t].items():
+            ids[t, g] = rng.choice(np.array(u), size=2, replace=False)
+    run = harness.DgRun(m, residents_per_layer=3, max_ids=2, wb_defer=1)
+    try:
+        P = G * U - len(run.resident_keys)
+        cfg = runtime.replay_config([U] * G, list(m.part_bytes), persistent_slots=len(run.resident_keys) + G,
+                                    bank_slots=2, blocks=P + G, spare_target=G, order=run.resident_keys, tokens=T,
+                                    n_ids=2, wb_defer=1, resident_events=events)
+        t_ref, s_ref = oracle.ref_replay(cfg, ids)
+        want = expected_sums(m, orc)
+        for t in range(T):
+            held = [g in held_at[t] for g in range(G)]
+            got = run.step(ids[t], held=held)
+            keys = np.arange(G)[:, None] * U + ids[t]
+            assert np.array_equal(got, want[keys]), "token %d read wrong bytes" % t
+            for te, g, u in events:
+                if te == t:
+                    run.ctx.make_resident(g, u)
+            assert np.array_equal(run.ctx.table(run.keys), t_ref[t]), "slot table differs after token %d" % t
+            run.ctx.check()
+        st = run.ctx.stats()
+        assert st["resident_units"] > 0 and st["misses"] == s_ref[-1][2]
+    finally:
+        run.close()
+
+
 def file_tier_run(m, R=3, pinned=4, S=3, **kw):
     """A DgRun with the file tier: per layer units [0, R) resident, [R, R + pinned) pinned, the rest in the model file
     only (tier DISK)."""

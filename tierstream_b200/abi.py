@@ -224,6 +224,7 @@ _PROTOS = {
     "ss_dg_enqueue_wait": (C.c_int, [vp, C.c_int, vp]),
     "ss_dg_enqueue_end": (C.c_int, [vp, vp]),
     "ss_dg_keep": (C.c_int, [vp, C.c_int, P(i32), C.c_int]),
+    "ss_dg_make_resident": (C.c_int, [vp, C.c_int, P(i32), C.c_int]),
     "ss_dg_residency": (C.c_int, [vp, P(ss_dg_unit), u32, P(u32)]),
     "ss_dg_set_sched": (C.c_int, [vp, u32, u32]),
     "ss_dg_set_budgets": (C.c_int, [vp, u32, u32, u32]),
@@ -281,7 +282,7 @@ _PROTOS = {
 }
 
 _ENGINE_PROTOS = {
-    "tse_capture_token": (C.c_int, [vp, u32, vp, u32, vp, u32, vp, u32, C.c_int, C.c_int, vp, P(vp)]),
+    "tse_capture_token": (C.c_int, [vp, u32, vp, u32, vp, u32, vp, u32, C.c_int, C.c_int, vp, P(vp), vp]),
     "tse_launch": (C.c_int, [vp, vp]),
     "tse_destroy": (C.c_int, [vp]),
     "tse_read_units": (C.c_int, [vp, u32, vp, u32, vp, u32, C.c_int, vp]),

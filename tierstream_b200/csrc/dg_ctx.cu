@@ -1803,15 +1803,33 @@ class CudaDgContext final : public DgContext {
         pieces.push_back({files_[size_t(p.source)].get(), base + o, std::min(kReadPiece, p.bytes - o), dst + at + o});
       at += p.bytes;
     }
+    const bool check = o_.verify_hash && !l.hash.empty();
+    Xxh64State h(0);
+    size_t hashed = 0;  // pieces fed to the hash, in unit order
     if (pool) {
-      pool->run(pieces.size(), [&](size_t i) { pieces[i].f->read(pieces[i].dst, pieces[i].off, pieces[i].bytes); });
+      // the hash runs while later pieces are still being read: a reader that finishes a piece advances it over the
+      // finished prefix unless another reader is already doing so; what is left is fed below
+      std::unique_ptr<std::atomic<uint8_t>[]> done(new std::atomic<uint8_t>[pieces.size()]());
+      std::mutex hashing;
+      pool->run(pieces.size(), [&](size_t i) {
+        pieces[i].f->read(pieces[i].dst, pieces[i].off, pieces[i].bytes);
+        done[i].store(1, std::memory_order_release);
+        if (!check) return;
+        std::unique_lock<std::mutex> lk(hashing, std::try_to_lock);
+        if (!lk.owns_lock()) return;
+        while (hashed < pieces.size() && done[hashed].load(std::memory_order_acquire)) {
+          h.feed(pieces[hashed].dst, size_t(pieces[hashed].bytes));
+          ++hashed;
+        }
+      });
     } else {
       for (const Piece& q : pieces) q.f->read(q.dst, q.off, q.bytes);
     }
-    if (o_.verify_hash && !l.hash.empty())
-      require(xxh64(dst, size_t(x_.unit_bytes)) == l.hash[size_t(unit)], SS_E_HASH,
-              "device-gated: unit (" + std::to_string(layer) + ", " + std::to_string(unit) +
-                  ") bytes differ from the descriptor hash");
+    if (!check) return;
+    for (; hashed < pieces.size(); ++hashed) h.feed(pieces[hashed].dst, size_t(pieces[hashed].bytes));
+    require(h.digest() == l.hash[size_t(unit)], SS_E_HASH,
+            "device-gated: unit (" + std::to_string(layer) + ", " + std::to_string(unit) +
+                ") bytes differ from the descriptor hash");
   }
 
   void init() {

@@ -184,11 +184,14 @@ extern "C" {
 // Captures one token step into a graph on `stream`: for gated layer g its n_ids ids are ids_dev[g * n_ids ..], its
 // results out_dev[g * n_ids ..] (zeroed by the graph first). slices: blocks per unit for the reader. n_pred > 0: each
 // layer g < G - 1 also predicts layer g + 1 from pred_dev[g * n_pred ..] on a forked branch joined before the next
-// export. Returns 0 or an error (cudaError_t, or 1000 + ss_status) and the instantiated graph in *exec_out.
+// export. held (host, n_gated flags, may be NULL): layers held resident by ss_dg_make_resident, which an engine
+// neither exports nor waits for: their reader resolves the ids through the table directly (a layer before a held one
+// predicts nothing). Returns 0 or an error (cudaError_t, or 1000 + ss_status) and the instantiated graph in *exec_out.
 __attribute__((visibility("default"))) int tse_capture_token(ss_ctx* c, uint32_t n_gated, const int32_t* ids_dev,
                                                              uint32_t n_ids, const int32_t* pred_dev, uint32_t n_pred,
                                                              unsigned long long* out_dev, uint32_t slices, int mode,
-                                                             int with_reader, void* stream, void** exec_out) {
+                                                             int with_reader, void* stream, void** exec_out,
+                                                             const uint8_t* held) {
   ss_dg_device_view v;
   SS(ss_dg_get_device_view(c, &v));
   cudaStream_t s = static_cast<cudaStream_t>(stream);
@@ -212,19 +215,21 @@ __attribute__((visibility("default"))) int tse_capture_token(ss_ctx* c, uint32_t
       break;
     }
     for (uint32_t g = 0; g < n_gated && !err; ++g) {
-      const int np = (n_pred && g + 1 < n_gated) ? int(n_pred) : 0;
-      if (ss_dg_enqueue_export(c, int(g), ids_dev + size_t(g) * n_ids, int(n_ids), np, s) != SS_OK) err = 1002;
-      if (!err && np) {
+      const bool is_held = held && held[g];
+      const int np = (n_pred && g + 1 < n_gated && !(held && held[g + 1])) ? int(n_pred) : 0;
+      if (!is_held && ss_dg_enqueue_export(c, int(g), ids_dev + size_t(g) * n_ids, int(n_ids), np, s) != SS_OK)
+        err = 1002;
+      if (!err && np && !is_held) {
         if (cudaEventRecord(fork, s) != cudaSuccess || cudaStreamWaitEvent(side, fork, 0) != cudaSuccess) err = 2;
         if (!err && ss_dg_enqueue_predict(c, int(g), pred_dev + size_t(g) * n_pred, np, side) != SS_OK) err = 1003;
       }
-      if (!err && ss_dg_enqueue_wait(c, int(g), s) != SS_OK) err = 1004;
+      if (!err && !is_held && ss_dg_enqueue_wait(c, int(g), s) != SS_OK) err = 1004;
       if (!err && with_reader) {
         reader_kernel<<<dim3(n_ids, slices), kThreads, 0, s>>>(v, g, ids_dev + size_t(g) * n_ids, n_ids,
                                                               out_dev + size_t(g) * n_ids, mode);
         if (cudaGetLastError() != cudaSuccess) err = 3;
       }
-      if (!err && np) {
+      if (!err && np && !is_held) {
         if (cudaEventRecord(join, side) != cudaSuccess || cudaStreamWaitEvent(s, join, 0) != cudaSuccess) err = 4;
       }
     }

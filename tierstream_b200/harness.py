@@ -87,7 +87,7 @@ class DgRun:
         G, U = model.layers, model.units
         if predict_prev:
             n_pred = max_ids
-        self.G, self.U, self.n_ids, self.n_pred = G, U, max_ids, n_pred
+        self.G, self.U, self.n_ids, self.n_pred, self.mode = G, U, max_ids, n_pred, mode
         s = DgSetup(model, max_ids=max_ids, **setup)
         self.setup = s
         self.desc, self.plan, o = s.desc, s.plan, s.options
@@ -107,22 +107,24 @@ class DgRun:
                                         self.stream.cuda_stream, slices=slices, mode=mode, pred_dev=pred_ptr,
                                         n_pred=n_pred, with_reader=with_reader)
         self.keys = G * U
-        self.graphs = {mode: self.graph}
+        self.graphs = {(mode, None): self.graph}
         self._graph_args = dict(slices=slices, pred_dev=pred_ptr, n_pred=n_pred, with_reader=with_reader)
 
-    def graph_for(self, mode):
+    def graph_for(self, mode, held=None):
         """The token graph whose readers check in `mode` (0: positional checksum, 1: word sum), captured on first use
-        on the same context, buffers and stream."""
-        if mode not in self.graphs:
-            self.graphs[mode] = runtime.TokenGraph(self.ctx, self.G, self.ids_dev.data_ptr(), self.n_ids,
-                                                   self.out_dev.data_ptr(), self.stream.cuda_stream, mode=mode,
-                                                   **self._graph_args)
-        return self.graphs[mode]
+        on the same context, buffers and stream; held: per gated layer, held resident (not exported, read directly)."""
+        key = (mode, tuple(bool(h) for h in held) if held is not None and any(held) else None)
+        if key not in self.graphs:
+            self.graphs[key] = runtime.TokenGraph(self.ctx, self.G, self.ids_dev.data_ptr(), self.n_ids,
+                                                  self.out_dev.data_ptr(), self.stream.cuda_stream, mode=mode,
+                                                  held=key[1], **self._graph_args)
+        return self.graphs[key]
 
-    def step(self, ids, preds=None, sync=True, mode=None):
+    def step(self, ids, preds=None, sync=True, mode=None, held=None):
         """One token: routed ids [G][max_ids] (and predictions [G][n_pred]); returns the readers' checksums (in `mode`,
-        default the graph's of the open)."""
-        graph = self.graph if mode is None else self.graph_for(mode)
+        default the graph's of the open). held: the layers held by ss_dg_make_resident (their ids must be held units)."""
+        graph = self.graph if mode is None and held is None else self.graph_for(self.mode if mode is None else mode,
+                                                                                held)
         self.ids_pin.numpy()[:] = np.asarray(ids, dtype=np.int32).reshape(-1)
         if preds is not None:
             self.pred_pin.numpy()[:self.G * self.n_pred] = np.asarray(preds, dtype=np.int32).reshape(-1)

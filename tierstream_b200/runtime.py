@@ -111,6 +111,13 @@ class DgContext:
         abi.check(abi.load().ss_stats_to_json(self.h, C.byref(p), C.byref(n)))
         return abi.take_text(p, n.value)
 
+    def make_resident(self, g, ids):
+        """ss_dg_make_resident: gated layer g's units `ids` on the device and kept there (not exported while held);
+        no ids releases the layer."""
+        a = np.ascontiguousarray(ids, dtype=np.int32)
+        abi.check(abi.load().ss_dg_make_resident(self.h, g, a.ctypes.data_as(C.POINTER(C.c_int32)) if a.size else None,
+                                                 a.size))
+
     def table(self, keys):
         out = np.empty(keys, dtype=np.int32)
         abi.check(abi.load().tsb_test_dg_table(self.h, out.ctypes.data_as(C.POINTER(C.c_int32)), keys))
@@ -244,12 +251,13 @@ class TokenGraph:
     """One decode step captured once (libtsb_engine.so): begin, per layer export / wait / reader, end."""
 
     def __init__(self, ctx, n_gated, ids_dev, n_ids, out_dev, stream, slices=64, mode=0, pred_dev=0, n_pred=0,
-                 with_reader=True):
+                 with_reader=True, held=None):
         eng = abi.load_engine()
         self.exec = C.c_void_p()
         self.stream = stream
+        h = (C.c_uint8 * n_gated)(*[1 if x else 0 for x in held]) if held is not None else None
         rc = eng.tse_capture_token(ctx.h, n_gated, ids_dev, n_ids, pred_dev or None, n_pred, out_dev, slices, mode,
-                                   1 if with_reader else 0, stream, C.byref(self.exec))
+                                   1 if with_reader else 0, stream, C.byref(self.exec), h)
         if rc != 0:
             msg = abi.load().ss_last_error().decode(errors="replace") if rc >= 1000 else ""
             raise RuntimeError("tse_capture_token failed: %d %s" % (rc, msg))
