@@ -77,21 +77,23 @@ def test_bytes_and_tables_match_reference(small_model, orc, ref, monkeypatch, co
         run.close()
 
 
-def test_c2_part_size_copy_engines_match_reference(orc, ref, monkeypatch):
-    """The benchmark's part size (3 x 33,030,144-byte parts, a 99 MB expert) on the copy-engine
-    mover with stream-written entries and ready words: 4 layers x 8 experts, 3 residents and 1 spare slot per layer,
-    Zipf(1.1) top-2, descriptor hashes checked at the open. After every token the device's slot table equals the
-    reference DgCore's replay, and every routed unit read through the table has the oracle's checksum of its source
-    bytes."""
+@pytest.mark.parametrize("mode,label", [("ce", "copy-engine"), ("kernel", "land-kernel")])
+def test_c2_part_size_movers_match_reference(orc, ref, monkeypatch, mode, label):
+    """The benchmark's part size (3 x 33,030,144-byte parts, a 99 MB expert) on both movers: the
+    copy engines with stream-written entries and ready words, and the land kernel, whose batches of such parts are cut
+    into 4 MiB pieces taken round-robin: 4 layers x 8 experts, 3 residents and 1 spare slot per layer, Zipf(1.1)
+    top-2, descriptor hashes checked at the open and every landing hashed on the device. After every token the
+    device's slot table equals the reference DgCore's replay, and every routed unit read through the table has the
+    oracle's checksum of its source bytes."""
     monkeypatch.setenv("TSB_DG_DETERMINISTIC", "1")
-    monkeypatch.setenv("TSB_COPY_MODE", "ce")
+    monkeypatch.setenv("TSB_COPY_MODE", mode)
     path = os.path.join(harness.model_dir(), "tsb-test-c2-parts.bin")
     m = synth.Model(path, layers=4, units=8, part_bytes=(33030144,) * 3, seed=7, top_k=2, with_hash=True)
     m.write()
     ids = synth.zipf_trace(24, m.layers, m.units, 2, s=1.1, seed=21)
     run = harness.DgRun(m, residents_per_layer=3, max_ids=2, verify=True)
     try:
-        assert '"copy":"copy-engine"' in run.ctx.stats_json()
+        assert '"copy":"%s"' % label in run.ctx.stats_json()
         want = {}
         buf = np.empty(m.unit_bytes, dtype=np.uint8)
         for k in np.unique((np.arange(m.layers)[None, :, None] * m.units + ids).reshape(-1)):

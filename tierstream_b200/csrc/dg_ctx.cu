@@ -365,6 +365,7 @@ class CudaMover final : public Mover {
     // TSB_COPY_MODE=kernel | ce forces one mover, TSB_CE_MIN_BYTES moves the threshold
     ce_min_ = uint64_t(8) << 20;
     if (const char* e = std::getenv("TSB_CE_MIN_BYTES")) ce_min_ = std::strtoull(e, nullptr, 10);
+    if (const char* e = std::getenv("TSB_LAND_INTERLEAVE")) interleave_ = std::strcmp(e, "0") != 0;
     if (const char* e = std::getenv("TSB_COPY_MODE")) {
       if (!std::strcmp(e, "kernel")) ce_min_ = UINT64_MAX;
       else if (!std::strcmp(e, "ce")) ce_min_ = 0;
@@ -820,6 +821,35 @@ class CudaMover final : public Mover {
     }
     add_copy(s, src, dst, bytes);
   }
+  // The land kernel's blocks take a batch's 64 KiB chunks in list order, so at any moment nearly all of them read the
+  // first copy. With copies from different sources (peers' stores over NVLink, this GPU's own store, pinned memory),
+  // that leaves one source busy and the others idle for this batch while other GPUs contend for it; cutting the
+  // copies into 4 MiB pieces taken round-robin keeps every source of the batch in flight at once. Left as it is when
+  // the pieces would not fit the batch.
+  static void interleave(dev::Batch& b) {
+    constexpr uint64_t kPiece = uint64_t(4) << 20;
+    if (b.n_copies < 2) return;
+    uint64_t pieces = 0;
+    for (uint32_t c = 0; c < b.n_copies; ++c) pieces += (b.copies[c].bytes + kPiece - 1) / kPiece;
+    if (pieces <= b.n_copies || pieces > dev::kMaxCopies) return;
+    dev::Copy whole[dev::kMaxCopies];
+    std::copy(b.copies, b.copies + b.n_copies, whole);
+    const uint32_t n = b.n_copies;
+    uint64_t off[dev::kMaxCopies] = {};
+    uint32_t out = 0;
+    for (bool more = true; more;) {
+      more = false;
+      for (uint32_t c = 0; c < n; ++c) {
+        if (off[c] >= whole[c].bytes) continue;
+        const uint64_t len = std::min(kPiece, whole[c].bytes - off[c]);
+        b.copies[out++] = {static_cast<const char*>(whole[c].src) + off[c], static_cast<char*>(whole[c].dst) + off[c],
+                           len};
+        off[c] += len;
+        more = true;
+      }
+    }
+    b.n_copies = out;
+  }
   void add_copy(Stream s, const char* src, char* dst, uint64_t bytes) {
     dev::Batch& b = *batch_[s];
     if (b.n_copies == dev::kMaxCopies) flush(s);
@@ -831,6 +861,7 @@ class CudaMover final : public Mover {
     if (!b.n_copies && !b.n_entries && !b.ready_word && !force) return;
     b.slot_of = b_.slot_of;
     b.done_counter = b_.counters + s;
+    if (interleave_) interleave(b);
     const int blocks = int(std::min<uint64_t>(std::max<uint64_t>(chunks_[s], 1), 296));
     ck_launch(dev::launch_batch(b, blocks, s_[s]), "land kernel");
     ++launches_;
@@ -850,6 +881,7 @@ class CudaMover final : public Mover {
   std::unique_ptr<dev::Batch> batch_[3];
   uint64_t chunks_[3] = {0, 0, 0};
   uint64_t ce_min_ = 0;
+  bool interleave_ = true;  // a batch's large copies cut in 4 MiB pieces, taken round-robin (TSB_LAND_INTERLEAVE=0: off)
   uint64_t launches_ = 0;
   bool deterministic_ = false;
   std::vector<cudaEvent_t> ev_a_, ev_b_;
