@@ -79,3 +79,49 @@ def test_static_table_matches_caller_scratch_twice(orc):
         got_b = [int(x) for x in out_b.cpu().numpy().view(np.uint64)]
         assert got_b == got_a == want
         assert int(mism_b.item()) == int(mism_a.item()) == 1
+
+
+_DEVICE1_FIRST = r"""
+import json, sys
+import numpy as np
+import torch
+sys.path.insert(0, sys.argv[1])
+sys.path.insert(0, sys.argv[1] + "/tests")
+from tierstream_b200 import abi
+from test_zz_no_alloc import _tables
+torch.cuda.set_device(1)  # nothing of the library has run on any device of this process yet
+h = np.random.default_rng(13).integers(0, 256, size=(2 << 20) + 64, dtype=np.uint8)
+data = torch.from_numpy(h).cuda()
+base = data.data_ptr()
+units = [[(base, 1 << 20)], [(base + (1 << 20), (1 << 20) + 64)]]
+spans, sb, ns = _tables(units)
+out = torch.zeros(2, dtype=torch.int64, device="cuda")
+s = torch.cuda.Stream()
+s.wait_stream(torch.cuda.current_stream())
+got = []
+for _ in range(2):  # two calls in a row on device 1
+    abi.check(abi.load().tsb_xxh64_units_static(spans, sb, ns, 2, None, out.data_ptr(), None, s.cuda_stream))
+    got.append([int(x) for x in out.cpu().numpy().view(np.uint64)])
+print(json.dumps(got))
+"""
+
+
+@pytest.mark.gpu
+def test_static_table_on_a_second_device_first(orc):
+    """tsb_xxh64_units_static whose first call in a fresh process is on device 1 (its table looked up and its kernel's
+    shared-memory attribute raised there, for that device): twice in a row, the oracle's hashes."""
+    torch = pytest.importorskip("torch")
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    import json
+    import os
+    import subprocess
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    r = subprocess.run([sys.executable, "-c", _DEVICE1_FIRST, root], capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stderr[-2000:]
+    got = json.loads(r.stdout.strip().splitlines()[-1])
+    h = np.random.default_rng(13).integers(0, 256, size=(2 << 20) + 64, dtype=np.uint8)
+    a, b = np.ascontiguousarray(h[:1 << 20]), np.ascontiguousarray(h[1 << 20:])
+    want = [orc.orc_xxh64(a.ctypes.data, a.size, 0), orc.orc_xxh64(b.ctypes.data, b.size, 0)]
+    assert got == [want, want]
