@@ -62,7 +62,9 @@ def args_():
     p.add_argument("--gpus", type=int, default=1)
     p.add_argument("--steps", type=int, default=None, help="timed steps (default: 64; c1-host 64, llama3-70b-host 12)")
     p.add_argument("--warmup", type=int, default=None, help="warm-up steps (default: 8; llama3-70b-host 3)")
-    p.add_argument("--impl", default="tierstream", choices=["tierstream", "reference"])
+    p.add_argument("--impl", default="tierstream", choices=["tierstream", "reference", "reference-cuda"],
+                   help="reference: the reference's CPU DgCore (the reference arm); reference-cuda (context only): the "
+                        "reference library built with its own CUDA backend, decoding on this GPU")
     p.add_argument("--copy-mode", default=os.environ.get("TSB_COPY_MODE", "auto"), choices=["auto", "kernel", "ce"])
     p.add_argument("--wb-defer", type=int, default=0,
                    help="ss_options.dg_wb_defer: 0 (here) enqueues a boundary's write-backs on the write-back stream "
@@ -448,6 +450,90 @@ def host_main(a):
     return 1 if bad else 0
 
 
+def reference_cuda_dir(model, setup, ids, want, n_ids):
+    """A directory of the files oracle/_ref/ref_dg_cuda opens: descriptor, tiers, budget and options (as bytes), the
+    shape, the trace and (when given) every key's expected word-sum checksum."""
+    d = tempfile.mkdtemp(prefix="tsb-refcu-")
+    with open(os.path.join(d, "desc.json"), "w") as f:
+        f.write(model.desc())
+    np.asarray(setup.tiers, dtype=np.uint8).tofile(os.path.join(d, "tiers.u8"))
+    with open(os.path.join(d, "budget.bin"), "wb") as f:
+        f.write(bytes(setup.budget))
+    with open(os.path.join(d, "options.bin"), "wb") as f:
+        f.write(bytes(setup.options))
+    with open(os.path.join(d, "meta.txt"), "w") as f:
+        f.write("%d %d %d\n" % (model.layers, model.units, n_ids))
+    np.ascontiguousarray(ids, dtype=np.int32).tofile(os.path.join(d, "ids.i32"))
+    if want is not None:
+        np.asarray(want, dtype=np.uint64).tofile(os.path.join(d, "want.u64"))
+    return d
+
+
+def run_reference_cuda(a):
+    """--impl reference-cuda, for context only: the reference library's own GPU decode on this B200
+    (oracle/_ref/ref_dg_cuda: its sources built with their CUDA backend for sm_100a, the ready word in mapped host
+    memory as the reference keeps it) driven by the same engine stand-in graph, on the same model, trace, options and
+    tokens as this library's line; its readers' checksums are compared with the generator's. Beside it, its
+    zero-miss protocol cost measured as this library's is (the graph less the readers alone, per layer)."""
+    if int(os.environ.get("RANK", "0")) != 0:
+        return 0
+    exe = os.path.join(ROOT, "oracle", "_ref", "ref_dg_cuda")
+    if not os.path.exists(exe):
+        print(json.dumps({"impl": "reference-cuda", "unavailable": "oracle/_ref/ref_dg_cuda (the reference's sources "
+                                                                   "built with their CUDA backend) is not built"}))
+        return 0
+    import shutil
+    import torch
+    from tierstream_b200 import harness, synth
+    torch.cuda.set_device(0)
+    model = synth.Model(model_path(), LAYERS, UNITS, [PART] * 3, seed=0, top_k=TOP_K, with_hash=True)
+    model.write()
+    model.hashes()
+    setup = harness.DgSetup(model, resident_keys=resident_keys(1), spare_per_layer=a.spare, max_ids=TOP_K,
+                            test_hooks=False, wb_defer=a.wb_defer, wb_stream=a.wb_stream, verify=True,
+                            inclusive=inclusive_of(a))
+    ids = synth.zipf_trace(a.warmup + a.steps, LAYERS, UNITS, TOP_K, s=ZIPF, seed=1)
+    want = harness.expected_sums(model, np.arange(LAYERS * UNITS), 1)
+    d = reference_cuda_dir(model, setup, ids, want, TOP_K)
+    try:
+        r = subprocess.run([exe, "stream", d, str(a.warmup), str(a.steps), "512"], capture_output=True, text=True,
+                           timeout=1200)
+    finally:
+        shutil.rmtree(d, ignore_errors=True)
+    got = [json.loads(x) for x in r.stdout.splitlines() if x.startswith("{")]
+    if r.returncode != 0 or not got or "value" not in got[-1]:
+        print(json.dumps({"impl": "reference-cuda", "error": (got[-1] if got else None),
+                          "stderr": r.stderr[-500:], "rc": r.returncode}))
+        return 1
+    line = got[-1]
+    # the zero-miss protocol cost on the model tierstream_b200/dg_overhead.py uses (32 x 8 units, 7 resident per layer,
+    # routes only to residents)
+    zm = synth.Model(os.path.join(harness.model_dir(), "tsb-overhead-32.bin"), layers=32, units=8,
+                     part_bytes=(256 << 10,) * 3, seed=9, top_k=2)
+    zm.write()
+    zs = harness.DgSetup(zm, residents_per_layer=7, spare_per_layer=1, max_ids=2, test_hooks=False)
+    d = reference_cuda_dir(zm, zs, np.tile(np.arange(2, dtype=np.int32), (32, 1))[None], None, 2)
+    try:
+        z = subprocess.run([exe, "zero", d, "100"], capture_output=True, text=True, timeout=600)
+    finally:
+        shutil.rmtree(d, ignore_errors=True)
+    zero = [json.loads(x) for x in z.stdout.splitlines() if x.startswith("{")]
+    out = {"impl": "reference-cuda", "metric": METRIC, "value": line["value"], "unit": "GB/s", "n_gpus": 1,
+           "steps": a.steps, "warmup": a.warmup, "ms_per_step": line["ms_per_step"], "higher_is_better": True,
+           "dtype": "u8", "data": "synthetic", "note": "context only: the reference library built with its own CUDA "
+                                                      "backend for sm_100a, on this GPU",
+           "config": {"workload": WORKLOAD, "layers": LAYERS, "experts": UNITS, "part_bytes": PART, "top_k": TOP_K,
+                      "zipf": ZIPF, "residents": RESIDENTS, "spare_slots_per_layer": a.spare,
+                      "wb_defer": a.wb_defer, "inclusive_blocks": inclusive_of(a)},
+           "misses_per_token": round(line["misses"] / max(1, a.warmup + a.steps), 3),
+           "verified": {"tokens": a.steps, "units": line["reads"], "mismatches": line["mismatches"]},
+           "dg_zero_miss": zero[-1] if zero else {"error": z.stderr[-300:]}}
+    if zero and "overhead_us_per_layer" in zero[-1]:
+        out["dg_zero_miss_us_per_layer"] = zero[-1]["overhead_us_per_layer"]
+    print(json.dumps(out))
+    return 1 if line["mismatches"] else 0
+
+
 def main():
     a = args_()
     if a.workload in HOST_WORKLOADS:
@@ -463,6 +549,8 @@ def main():
         a.spare = SPARE
     if a.impl == "reference":
         return run_reference(a)
+    if a.impl == "reference-cuda":
+        return run_reference_cuda(a)
     os.environ["TSB_COPY_MODE"] = a.copy_mode
     import torch
     from tierstream_b200 import abi, harness, synth
