@@ -492,6 +492,9 @@ def run_reference_cuda(a):
     setup = harness.DgSetup(model, resident_keys=resident_keys(1), spare_per_layer=a.spare, max_ids=TOP_K,
                             test_hooks=False, wb_defer=a.wb_defer, wb_stream=a.wb_stream, verify=True,
                             inclusive=inclusive_of(a))
+    # the reference's open reads the residents through a ring of 4 pinned buffers of at least a unit each, which it
+    # admits against the host budget on top of the pinned units (its dg_layout.cpp:425-443)
+    setup.budget.host_pinned_bytes += 4 * model.unit_bytes + (256 << 20)
     ids = synth.zipf_trace(a.warmup + a.steps, LAYERS, UNITS, TOP_K, s=ZIPF, seed=1)
     want = harness.expected_sums(model, np.arange(LAYERS * UNITS), 1)
     d = reference_cuda_dir(model, setup, ids, want, TOP_K)
@@ -512,6 +515,7 @@ def run_reference_cuda(a):
                      part_bytes=(256 << 10,) * 3, seed=9, top_k=2)
     zm.write()
     zs = harness.DgSetup(zm, residents_per_layer=7, spare_per_layer=1, max_ids=2, test_hooks=False)
+    zs.budget.host_pinned_bytes += 4 * zm.unit_bytes + (256 << 20)
     d = reference_cuda_dir(zm, zs, np.tile(np.arange(2, dtype=np.int32), (32, 1))[None], None, 2)
     try:
         z = subprocess.run([exe, "zero", d, "100"], capture_output=True, text=True, timeout=600)

@@ -42,6 +42,42 @@ def land(pairs, stream):
                                       stream.cuda_stream))
 
 
+def concurrent_h2d(host, dev, size):
+    """Pinned host -> HBM over the whole buffer in `size` parts, with the parts dealt round-robin to several movers
+    running at once (each on a stream of its own; the time from the first start to the last end): one copy-engine
+    stream, two, one with the land kernel, two with the land kernel. GB/s per arrangement."""
+    n = host.numel() // size
+    moved = n * size
+    streams = [torch.cuda.Stream() for _ in range(3)]
+    hp, dp = host.data_ptr(), dev.data_ptr()
+
+    def run(movers):
+        parts = [[i for i in range(n) if i % len(movers) == m] for m in range(len(movers))]
+        start = torch.cuda.Event()
+        start.record(streams[0])
+        ends = []
+        for m, kind in enumerate(movers):
+            st = streams[m]
+            st.wait_event(start)
+            with torch.cuda.stream(st):
+                if kind == "ce":
+                    for i in parts[m]:
+                        dev[i * size:(i + 1) * size].copy_(host[i * size:(i + 1) * size], non_blocking=True)
+                else:
+                    land([(hp + i * size, dp + i * size, size) for i in parts[m]], st)
+            e = torch.cuda.Event()
+            e.record(st)
+            ends.append(e)
+        for e in ends:
+            streams[0].wait_event(e)
+
+    out = {}
+    for name, movers in (("ce_1_stream", ["ce"]), ("ce_2_streams", ["ce", "ce"]), ("ce_and_kernel", ["ce", "kernel"]),
+                         ("ce_2_streams_and_kernel", ["ce", "ce", "kernel"])):
+        out[name] = round(moved / _time(lambda: run(movers), streams[0]) / 1e6, 2)
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--total-mib", type=int, default=1024)
@@ -80,6 +116,7 @@ def main():
         else:
             ce_min = None
     print(json.dumps({"suggested_ce_min_bytes": ce_min, "device": torch.cuda.get_device_name()}))
+    print(json.dumps({"h2d_concurrent_gbs": concurrent_h2d(host, dev, 33030144), "part_bytes": 33030144}))
 
 
 if __name__ == "__main__":
