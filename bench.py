@@ -133,6 +133,8 @@ def configure(a):
             g["LAYERS"] = a.layers
             g["RESIDENTS"] = a.layers * per_layer
             g["MODEL_FILE"] = shape["MODEL_FILE"].replace(".bin", "-%d.bin" % a.layers)
+        if a.tier == "file":  # every byte written (never the peer tier's sparse file of the same shape)
+            g["MODEL_FILE"] = g["MODEL_FILE"].replace(".bin", "-file.bin")
 
 
 class Clocks:
@@ -243,6 +245,19 @@ def disk_keys(a, residents):
         rest = [g * UNITS + e for e in pop[g] if g * UNITS + e not in res]
         out += rest[a.pinned_per_layer:]
     return out
+
+
+def host_hash_rate(unit, reps=3):
+    """GB/s of the library's host xxh64 over one unit-sized buffer on one thread (best of reps)."""
+    from tierstream_b200 import abi
+    buf = np.random.default_rng(0).integers(0, 256, size=unit, dtype=np.uint8)
+    best = None
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        abi.load().tsb_xxh64(buf.ctypes.data, buf.size, 0)
+        dt = time.perf_counter() - t0
+        best = dt if best is None else min(best, dt)
+    return unit / best / 1e9
 
 
 def file_read_peak(path, unit, units=20, threads=8):
@@ -562,8 +577,8 @@ def main():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     a.peer = a.tier == "peer" or (a.tier == "auto" and world > 1)
     a.file = a.tier == "file"
-    if a.file and (world > 1 or a.workload != "mixtral-8x7b-dg"):
-        raise SystemExit("--tier file runs the Mixtral-shaped workload on one GPU")
+    if a.file and (world > 1 or a.workload == "qwen3-235b-a22b-peer"):
+        raise SystemExit("--tier file runs the Mixtral- or DeepSeek-shaped workload (the latter with --layers) on one GPU")
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
@@ -577,7 +592,9 @@ def main():
         if dist:
             dist.barrier()
 
-    qwen = a.workload in DEVICE_FILLED
+    # the peer tier's Qwen3 and DeepSeek shapes write their stores from the generator over a sparse model file; with
+    # the file tier the model file holds every byte
+    qwen = a.workload in DEVICE_FILLED and not a.file
     # descriptor hashes (the stores' and the landings' checks on the device) for every model written to disk; the
     # Qwen3-shaped stores are written on the device from the generator and checked by the readers' sums instead
     hashed = not qwen
@@ -633,6 +650,7 @@ def main():
                         verify=hashed,
                         inclusive=inclusive, peer=setup.tier if setup else None,
                         disk_keys=disk_keys(a, resident_keys(1)) if a.file else (), disk_staging=a.staging,
+                        disk_prefetch=1 if a.file and RHO > 0 else 0,
                         disk_queue=a.disk_queue, policy={"lru": 0, "scored": 1, "scored_auto": 2}[a.policy],
                         predict_prev=RHO > 0)
     t_open = time.perf_counter() - t_open
@@ -835,21 +853,27 @@ def main():
         # several staging buffers the next miss's read runs while the last one's copy lands, so the ideal mover is
         # bound by the slower of the two rates
         rd = dg["disk_read_bytes"] / (dg["disk_read_ns"] / 1e9) / 1e9 if dg["disk_read_ns"] else None
-        peak_file = min(read_peak, peak) if read_peak and peak else None
-        line["config"].update({"workload": "mixtral-8x7b-dg-file", "pinned_per_layer": a.pinned_per_layer,
+        # with descriptor hashes every file read is hashed on the host as it is read (the reference's read_checked):
+        # a read then takes the longer of reading and hashing
+        hash_rate = host_hash_rate(unit) if hashed else None
+        bounds = [r for r in (read_peak, hash_rate, peak) if r]
+        peak_file = min(bounds) if len(bounds) >= 2 else None
+        line["config"].update({"workload": WORKLOAD.replace("-peer", "") + "-file", "pinned_per_layer": a.pinned_per_layer,
                                "staging": a.staging, "file_units": LAYERS * UNITS - RESIDENTS -
                                a.pinned_per_layer * LAYERS})
         line["file_tier"] = {"disk_read_gbs": round(rd, 3) if rd else None,
+                             "host_hash_gbs": round(hash_rate, 3) if hash_rate else None,
                              "file_read_peak_gbs": round(read_peak, 3) if read_peak else None,
                              "reads_per_token": round(dg["disk_reads"] / a.steps, 3)}
         line["roofline"].update({
             "bound": "file+link", "kernel": "miss service (file read into staging, then the copy, entries and ready)",
             "peak": round(peak_file, 3) if peak_file else None,
             "frac": round(achieved / peak_file, 4) if achieved and peak_file else None,
-            "peak_source": "the slower of the two rates measured in this run (a miss's read overlaps the previous "
-                           "miss's copy through the staging buffers): the model file read unit after unit as the "
-                           "file tier reads it (O_DIRECT, 8 MiB pieces, 8 reader threads), and the copy-engine "
-                           "pinned->HBM rate"})
+            "peak_source": "the slowest of the rates measured in this run (a miss's read overlaps the previous "
+                           "miss's copy through the staging buffers, and its host hash overlaps its own read): the "
+                           "model file read unit after unit as the file tier reads it (O_DIRECT, 8 MiB pieces, 8 "
+                           "reader threads), the host xxh64 of one unit on one thread (with descriptor hashes), and "
+                           "the copy-engine pinned->HBM rate"})
         a.no_cpu_baseline = True  # the reference arm's sample is the pinned-RAM configuration
     if not a.no_cpu_baseline and world == 1:
         # the reference arm's own measurement (same trace, tokens and warm-up subtraction)
