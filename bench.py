@@ -756,7 +756,7 @@ def main():
 
     # the device-gated protocol's cost per layer when nothing misses (a small all-resident model, dg_overhead)
     from tierstream_b200 import dg_overhead
-    zero_miss = dg_overhead.measure(layers=LAYERS, tokens=100, warmup=10)
+    zero_miss = dg_overhead.measure(layers=LAYERS, tokens=100, warmup=10) if rank == 0 else None
     tot = torch.tensor([moved, moved_e2e, dev_ms, e2e_s, dma_ms], dtype=torch.float64, device="cuda")
     ver = torch.tensor([2 * a.steps, n1 + n0, bad1 + bad0], dtype=torch.int64, device="cuda")
     if dist:
@@ -819,8 +819,10 @@ def main():
                                             "token graph (begin, per layer export -> wait -> reader, end) less the "
                                             "same readers captured alone, per layer; CUDA events, 100 tokens after 10 "
                                             "warm-up" % LAYERS),
-        "landing_check": dict(check, how="every unit copied into a slot hashed on the device (K3, xxh64) against "
-                                          "its descriptor hash on a low-priority stream behind the layer's ready word; "
+        "landing_check": dict(check, how="every unit copied into a slot from host memory (pinned blocks, file "
+                                          "staging) hashed on the device (K3, xxh64) against its descriptor hash on a "
+                                          "low-priority stream behind the layer's ready word (a copy from a peer store "
+                                          "is not: each store was hashed on the device when it was filled); "
                                           "a copy into a slot still being hashed waits for it (hold_waits); each "
                                           "ss_end waits for the previous token's hashes (end_wait)"),
         "clocks": clk, "open_s": round(t_open, 2), "open": open_stats, "dg": dg, "miss_layer_path": layer_path,

@@ -416,10 +416,13 @@ class CudaMover final : public Mover {
         }
       }
       ++(self ? self_units_ : peer_units_);
-    } else {
-      for (uint32_t p = 0; p < parts(); ++p)
-        copy(s, block_dev(block) + x_.part_offset[p], arena(p, slot), x_.part_bytes[p], cudaMemcpyHostToDevice);
+      // not hashed again on landing: the store was hashed on the device against the descriptor when it was filled and
+      // nothing writes it while decoding; a unit hashes in ~75 ms (four serial lane chains) while a peer-tier token
+      // lasts ~10 ms, so hashing store copies would hold their slots across several tokens
+      return;
     }
+    for (uint32_t p = 0; p < parts(); ++p)
+      copy(s, block_dev(block) + x_.part_offset[p], arena(p, slot), x_.part_bytes[p], cudaMemcpyHostToDevice);
     check_add(s, key, slot);
   }
   void d2h(Stream s, int32_t slot, int32_t block, int32_t part, uint32_t key) override {
@@ -615,8 +618,9 @@ class CudaMover final : public Mover {
   double dma_total_ms() const { return dma_total_ms_; }
 
   // ---- The landing check (verify_hash with descriptor hashes) ----
-  // Every unit copied into a slot (demand, prefetch, placement round, kept-resident set; from a pinned block, a staging
-  // buffer or a peer store) is hashed on the device by K3 over the landed slot, after the copies of its stream (after
+  // Every unit copied into a slot from host memory (demand, prefetch, placement round, kept-resident set; from a pinned
+  // block or a file's staging buffer) is hashed on the device by K3 over the landed slot, after the copies of its stream
+  // (a copy from a peer store is not: the store was hashed on the device when it was filled, see h2d) (after
   // the layer's ready word for demand copies, so the engine never waits for it), and compared with its descriptor hash;
   // a mismatch is logged in mapped memory for the host. One unit's hash is a serial chain (about 70 ms for a 99 MB
   // unit), so launches run side by side on a pool of low-priority streams, a launch on a stream whose last launch has

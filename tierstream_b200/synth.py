@@ -43,14 +43,15 @@ class Model:
         threads = threads or max(1, min(16, os.cpu_count() or 1))
         chunk = 1 << 28
         buf = np.empty(min(chunk, self.file_bytes), dtype=np.uint8)
-        with open(self.path + ".tmp", "wb") as f:
+        tmp = "%s.%d.tmp" % (self.path, os.getpid())  # (processes writing the same model each write their own)
+        with open(tmp, "wb") as f:
             pos = 0
             while pos < self.file_bytes:
                 n = min(chunk, self.file_bytes - pos)
                 eng.tse_fill_bytes(self.seed, pos, n, buf.ctypes.data, threads)
                 f.write(memoryview(buf)[:n])
                 pos += n
-        os.replace(self.path + ".tmp", self.path)
+        os.replace(tmp, self.path)
 
     def create_sparse(self):
         """A model file of the right size whose bytes are never read (the peer tier's stores are filled on the device
