@@ -138,14 +138,46 @@ def configure(a):
 
 
 class Clocks:
-    """nvidia-smi samples during the timed region (clocks and throttle reasons)."""
+    """SM clock and clock-event reasons sampled during the timed region: NVML read every 10 ms from a thread (read-only
+    queries; the device found by its UUID, so CUDA_VISIBLE_DEVICES cannot shift it), else nvidia-smi every 200 ms."""
 
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
          "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
          "clocks_event_reasons.sw_power_cap")
+    # NVML clock-event reason bits
+    BITS = {"sw_power_cap": 0x4, "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40}
 
     def __init__(self, index):
         self.index = index
+        self.sm, self.mx, self.reasons = [], None, set()
+        self.p = self.f = self.t = None
+        try:
+            import threading
+            import pynvml
+            import torch
+            pynvml.nvmlInit()
+            try:  # this process's CUDA device `index`, by its UUID
+                h = pynvml.nvmlDeviceGetHandleByUUID("GPU-" + str(torch.cuda.get_device_properties(index).uuid))
+            except Exception:
+                vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+                h = pynvml.nvmlDeviceGetHandleByIndex(int(vis.split(",")[index]) if vis else index)
+            self.mx = float(pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM))
+            self.stop_ev = threading.Event()
+
+            def run():
+                while not self.stop_ev.is_set():
+                    self.sm.append(float(pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)))
+                    bits = pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)
+                    for n, b in self.BITS.items():
+                        if bits & b:
+                            self.reasons.add(n)
+                    self.stop_ev.wait(0.01)
+
+            self.t = threading.Thread(target=run, daemon=True)
+            self.t.start()
+            return
+        except Exception:
+            self.t = None
         self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
         try:
             self.p = subprocess.Popen(["nvidia-smi", "--query-gpu=" + self.Q, "--format=csv,noheader,nounits",
@@ -154,6 +186,11 @@ class Clocks:
             self.p = None
 
     def stop(self):
+        if self.t is not None:
+            self.stop_ev.set()
+            self.t.join(5)
+            return {"sm_mhz": statistics.median(self.sm) if self.sm else None, "sm_max_mhz": self.mx,
+                    "reasons": sorted(self.reasons), "samples": len(self.sm), "source": "nvml, 10 ms"}
         if self.p:
             self.p.terminate()
             try:
@@ -177,7 +214,7 @@ class Clocks:
                     reasons.add(n)
         os.unlink(self.f.name)
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": len(sm)}
+                "samples": len(sm), "source": "nvidia-smi, 200 ms"}
 
 
 def h2d_peak(torch):
@@ -858,8 +895,13 @@ def main():
         # with descriptor hashes every file read is hashed on the host as it is read (the reference's read_checked):
         # a read then takes the longer of reading and hashing
         hash_rate = host_hash_rate(unit) if hashed else None
-        bounds = [r for r in (read_peak, hash_rate, peak) if r]
-        peak_file = min(bounds) if len(bounds) >= 2 else None
+        # an ideal mover serves the file misses at the slowest of read, hash and link, and the misses from pinned
+        # blocks at the link, in the proportion of rank 0's timed tokens
+        file_rate = min(r for r in (read_peak, hash_rate, peak) if r) if read_peak and peak else None
+        file_units = min(dg["disk_reads"], units_moved)
+        ideal_s = (file_units * unit / (file_rate * 1e9) + (units_moved - file_units) * unit / (peak * 1e9)
+                   if file_rate else 0)
+        peak_file = units_moved * unit / ideal_s / 1e9 if ideal_s > 0 else None
         line["config"].update({"workload": WORKLOAD.replace("-peer", "") + "-file", "pinned_per_layer": a.pinned_per_layer,
                                "staging": a.staging, "file_units": LAYERS * UNITS - RESIDENTS -
                                a.pinned_per_layer * LAYERS})
@@ -871,11 +913,12 @@ def main():
             "bound": "file+link", "kernel": "miss service (file read into staging, then the copy, entries and ready)",
             "peak": round(peak_file, 3) if peak_file else None,
             "frac": round(achieved / peak_file, 4) if achieved and peak_file else None,
-            "peak_source": "the slowest of the rates measured in this run (a miss's read overlaps the previous "
-                           "miss's copy through the staging buffers, and its host hash overlaps its own read): the "
-                           "model file read unit after unit as the file tier reads it (O_DIRECT, 8 MiB pieces, 8 "
-                           "reader threads), the host xxh64 of one unit on one thread (with descriptor hashes), and "
-                           "the copy-engine pinned->HBM rate"})
+            "peak_source": "rates measured in this run: a file miss at the slowest of the model file read unit "
+                           "after unit as the file tier reads it (O_DIRECT, 8 MiB pieces, 8 reader threads), the host "
+                           "xxh64 of one unit on one thread (with descriptor hashes; it overlaps the read) and the "
+                           "copy-engine pinned->HBM rate (a read overlaps the previous miss's copy through the staging "
+                           "buffers); a miss from a pinned block at that copy rate; blended in the proportion of rank "
+                           "0's timed tokens (%d file reads of %d units)" % (file_units, units_moved)})
         a.no_cpu_baseline = True  # the reference arm's sample is the pinned-RAM configuration
     if not a.no_cpu_baseline and world == 1:
         # the reference arm's own measurement (same trace, tokens and warm-up subtraction)
