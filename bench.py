@@ -149,7 +149,7 @@ class Clocks:
 
     def __init__(self, index):
         self.index = index
-        self.sm, self.mx, self.reasons = [], None, set()
+        self.sm, self.mx, self.reasons, self.failed = [], None, set(), False
         self.p = self.f = self.t = None
         try:
             import threading
@@ -166,11 +166,14 @@ class Clocks:
 
             def run():
                 while not self.stop_ev.is_set():
-                    self.sm.append(float(pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)))
-                    bits = pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)
-                    for n, b in self.BITS.items():
-                        if bits & b:
-                            self.reasons.add(n)
+                    try:
+                        self.sm.append(float(pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)))
+                        bits = pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)
+                        for n, b in self.BITS.items():
+                            if bits & b:
+                                self.reasons.add(n)
+                    except Exception:  # a query NVML refuses: the samples taken so far stand
+                        self.failed = True
                     self.stop_ev.wait(0.01)
 
             self.t = threading.Thread(target=run, daemon=True)
