@@ -105,6 +105,9 @@ def args_():
     p.add_argument("--layers", type=int, default=0,
                    help="qwen3 / deepseek only: fewer layers than the config's, for fewer GPUs (the "
                         "line then names the layer count; not the config's number)")
+    p.add_argument("--peer-layout", default="whole", choices=["whole", "striped"],
+                   help="peer tier stores: whole units at their owners, or every unit striped over all GPUs (a miss "
+                        "reads a stripe from each)")
     p.add_argument("--peer-copy", default="auto", choices=["auto", "kernel", "ce"],
                    help="peer tier mover: the copy engines, the land kernel's SM loads, or auto (the default): the "
                         "copy engines for the Mixtral shape (one or two misses a layer: 2,950 against 2,751 GB/s at "
@@ -669,7 +672,34 @@ def main():
         cal = synth.zipf_trace(64, LAYERS, UNITS, TOP_K, s=ZIPF, seed=1001 + rank, perm_seed=1 + rank, rho=RHO)
         counts = np.bincount((np.arange(LAYERS)[None, :, None] * UNITS + cal).reshape(-1), minlength=LAYERS * UNITS)
         filler = None
-        if qwen:
+        striped = a.peer_layout == "striped"
+        if qwen and striped:
+            def filler(store, owner):
+                # this rank's stripe of every owned unit written on the device from the model's byte generator, in
+                # store order (unit i at base + i * stripe); the first checked against the host generator
+                keys = np.nonzero(owner >= 0)[0]
+                stripe = peer_mod.stripe_bytes(model.unit_bytes, world)
+                lo, n = peer_mod.stripe_range(model.unit_bytes, world, rank)
+                if not keys.size or not n:
+                    return
+                offs = np.array([model.unit_offset(int(k) // UNITS, int(k) % UNITS) + lo for k in keys],
+                                dtype=np.uint64)
+                s = torch.cuda.Stream()
+                fill = abi.load_engine().tse_fill_units_device
+                if n == stripe:
+                    rc = fill(model.seed, offs.ctypes.data_as(C.POINTER(C.c_uint64)), keys.size, n, store.base,
+                              s.cuda_stream)
+                else:  # a shorter last stripe: one unit at a time at the store's stride
+                    rc = 0
+                    for i in range(keys.size):
+                        rc = rc or fill(model.seed, offs[i:].ctypes.data_as(C.POINTER(C.c_uint64)), 1, n,
+                                        store.base + i * stripe, s.cuda_stream)
+                assert rc == 0, "device fill failed: %d" % rc
+                s.synchronize()
+                k0 = int(keys[0])
+                want = model.unit_bytes_of(k0 // UNITS, k0 % UNITS)[lo:lo + n]
+                assert np.array_equal(peer_mod.read_device(store.base, n), want), "store fill differs"
+        elif qwen:
             def filler(store, owner):
                 # every owned unit written on the device from the model's byte generator, in store order; the first
                 # one checked against the host generator
@@ -687,7 +717,8 @@ def main():
                 assert np.array_equal(first, model.unit_bytes_of(k0 // UNITS, k0 % UNITS)), "store fill differs"
         setup = peer_mod.PeerSetup(runtime.Desc(model.desc()), counts, dist, world, rank, local, verify=hashed,
                                    copy=1 if a.peer_copy == "ce" else 0,
-                                   collective_device=torch.device("cuda", local) if dist else None, filler=filler)
+                                   collective_device=torch.device("cuda", local) if dist else None, filler=filler,
+                                   layout=abi.PEER_STRIPED if striped else abi.PEER_WHOLE_UNITS)
     # verify_hash with descriptor hashes: residents checked at the open, and every unit landed in a slot while decoding
     # hashed on the device against its descriptor hash (the landing check)
     run = harness.DgRun(model, resident_keys=resident_keys(1 + rank), spare_per_layer=a.spare, max_ids=TOP_K,
@@ -753,6 +784,8 @@ def main():
                  "end_wait_ms_per_token": round((c1["end_wait_s"] - c0["end_wait_s"]) * 1e3 / a.steps, 3)}
         peer_units = f1["peer"]["peer_units"] - f0["peer"]["peer_units"]
         self_units = f1["peer"]["self_units"] - f0["peer"]["self_units"]
+        peer_bytes = f1["peer"]["peer_bytes"] - f0["peer"]["peer_bytes"]
+        self_bytes = f1["peer"]["self_bytes"] - f0["peer"]["self_bytes"]
         units_moved = (s1["fetched"] - s0["fetched"]) + (s1["prefetched"] - s0["prefetched"])
         moved = units_moved * unit
         dma_ms = j1["dma_ms_total"] - j0["dma_ms_total"]
@@ -876,25 +909,31 @@ def main():
                     "disk_queue": a.disk_queue},
     }
     if a.peer:
-        # every expert lives in one rank's store: a miss is an NVLink pull from a peer or an HBM copy from the
-        # rank's own store; no pinned RAM is allocated
+        # every expert lives in one rank's store (striped: a stripe of it in every rank's store): a miss is an NVLink
+        # pull from a peer or an HBM copy from the rank's own store (striped: both); no pinned RAM is allocated
         line["config"].update({"workload": WORKLOAD if qwen else "mixtral-8x7b-dg-peer",
                                "parallelism": "peer tier x%d" % world,
-                               "peer_copy": a.peer_copy})
-        line["peer"] = dict(peer_stats, timed_peer_units=peer_units, timed_self_units=self_units)
-        # the demand stream moves peer units over NVLink and own-store units inside HBM in the same time: the peak is
-        # the rate of an ideal mover doing both, each at its measured rate
+                               "peer_copy": a.peer_copy, "peer_layout": a.peer_layout})
+        line["peer"] = dict(peer_stats, timed_peer_units=peer_units, timed_self_units=self_units,
+                            timed_peer_bytes=peer_bytes, timed_self_bytes=self_bytes,
+                            checked_units=setup.checked_units)
+        # whole units: a missing unit comes from one store, a peer's over NVLink or the rank's own inside HBM, and the
+        # peak is the rate of an ideal mover doing both kinds in turn, each at its measured rate; striped: every unit's
+        # stripes are pulled together, so the ideal mover overlaps them and is bound by the slower of the two
         hbm_copy = hbm_copy_peak()
-        ideal_s = (peer_units * unit / 770e9) + (self_units * unit / (hbm_copy * 1e9))
-        peak_mix = (peer_units + self_units) * unit / ideal_s / 1e9 if ideal_s > 0 else None
+        parts_s = (peer_bytes / 770e9, self_bytes / (hbm_copy * 1e9))
+        ideal_s = max(parts_s) if striped else sum(parts_s)
+        peak_mix = (peer_bytes + self_bytes) / ideal_s / 1e9 if ideal_s > 0 else None
         line["roofline"].update({
             "bound": "nvlink+hbm", "kernel": "miss service from the stores (peer pulls over NVLink + own-store copies)",
             "peak": round(peak_mix, 3) if peak_mix else None,
             "frac": round(achieved / peak_mix, 4) if achieved and peak_mix else None,
-            "peak_source": "blend of the peer copy 770 GB/s per direction measured on this pool (MEASURED_PEAKS.json "
-                           "has no NVLink figure) for the %d units pulled from peers and the measured HBM copy rate "
-                           "(MEASURED_PEAKS.json hbm_gbs / 2 = %.1f GB/s) for the %d units copied from the rank's own "
-                           "store, rank 0's timed tokens" % (peer_units, hbm_copy, self_units)})
+            "peak_source": "%s of the peer copy 770 GB/s per direction measured on this pool (MEASURED_PEAKS.json "
+                           "has no NVLink figure) for the %.2f GB pulled from peers and the measured HBM copy rate "
+                           "(MEASURED_PEAKS.json hbm_gbs / 2 = %.1f GB/s) for the %.2f GB copied from the rank's own "
+                           "store, rank 0's timed tokens" % ("the slower (stripes pulled together)" if striped else
+                                                             "blend (sum of times)", peer_bytes / 1e9, hbm_copy,
+                                                             self_bytes / 1e9)})
     if a.file:
         # a file miss is a synchronous O_DIRECT read into a staging buffer, then its copy to HBM on a copy stream; with
         # several staging buffers the next miss's read runs while the last one's copy lands, so the ideal mover is

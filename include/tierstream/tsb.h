@@ -279,12 +279,35 @@ typedef struct tsb_peer_tier {
   const int32_t* owner;     /* [keys] owning rank, -1 = pinned RAM */
   void* const* store_base;  /* [world] each rank's store as seen from this process (its own included) */
   uint32_t copy;            /* 0: the land kernel pulls the parts (SM loads), 1: the copy engines */
-  uint32_t reserved;
+  uint32_t layout;          /* TSB_PEER_WHOLE_UNITS (0) or TSB_PEER_STRIPED (1): how the stores hold the units */
 } tsb_peer_tier;
 /* ss_open (device-gated forward mode) with the peer tier. Every store must stay allocated and mapped until
  * ss_close. */
 SS_API ss_status tsb_open_peer(const ss_desc* d, const ss_budget* budget, const ss_plan* plan, const ss_options* opt,
                                const tsb_peer_tier* peer, ss_ctx** out);
+
+/* The striped layout (tsb_peer_tier.layout = TSB_PEER_STRIPED): every owned unit is cut into `world` stripes of
+ * tsb_peer_stripe_bytes(unit_bytes, world) bytes (ceil(unit_bytes / world) rounded up to 256; the last ones shorter or
+ * empty), stripe r covering [r x stripe, min(unit_bytes, (r + 1) x stripe)) of the unit's bytes (parts back to back),
+ * and stripe r of every owned unit lives in rank r's store, unit i (its position among all owned keys, key order) at
+ * base + i x stripe. A miss then copies 1/world of the unit from every GPU at once (the next rank's stripe first, its
+ * own last), so the ranks' pulls are spread over every GPU's links instead of queueing on the owners of the units
+ * they miss. The owner map only says which units are in the tier; tsb_peer_store_migrate refuses striped stores (a
+ * re-plan that keeps the owned units keeps them as they are). */
+#define TSB_PEER_WHOLE_UNITS 0
+#define TSB_PEER_STRIPED 1
+SS_API uint64_t tsb_peer_stripe_bytes(uint64_t unit_bytes, uint32_t world);
+/* This rank's striped store on `device`: stripe `rank` of every unit with owner[k] >= 0, read from the descriptor's
+ * sources (fill != 0) or only allocated (fill = 0: the caller writes each stripe at base + i x stripe). NULL base when
+ * this rank's stripe is empty or no unit is owned. A stripe is not checked on its own: see tsb_peer_tier_verify. */
+SS_API ss_status tsb_peer_store_create_striped(const ss_desc* d, const int32_t* owner, uint32_t keys, int32_t rank,
+                                               uint32_t world, int device, int fill, tsb_peer_store** out);
+/* The tier against the descriptor's hashes, this rank's share: the owned units whose position among the owned keys is
+ * rank modulo world, each gathered whole from the stores as the tier maps them (peers' over NVLink) into scratch on
+ * `device` (at most 2 GiB) and hashed there (K3). Call on every rank once every store is written and mapped; together
+ * the ranks check each owned unit once, in either layout. SS_E_HASH on a mismatch; checked_units (may be NULL). */
+SS_API ss_status tsb_peer_tier_verify(const ss_desc* d, const tsb_peer_tier* peer, int device,
+                                      uint64_t* checked_units);
 
 /* A re-plan (after a new all-reduce of routing counts and tsb_peer_plan): dst, allocated by tsb_peer_store_alloc for
  * the new owners, is filled with its units from where they live now (old_owner, old_base[world]: every rank's current

@@ -97,6 +97,102 @@ def test_emulated_two_ranks(model, orc, monkeypatch, copy, mixed):
             s.close()
 
 
+@pytest.mark.parametrize("world", [2, 3])
+@pytest.mark.parametrize("copy", [0, 1])
+@pytest.mark.parametrize("mixed", [False, True])
+def test_striped_emulated_ranks(model, orc, monkeypatch, world, copy, mixed):
+    """The striped layout on one GPU: `world` stores, each holding one stripe of every owned unit (world = 3 gives
+    2,816-byte stripes whose edges fall inside the 2,048 / 2,048 / 4,096-byte parts, the last stripe 2,560 bytes).
+    The ranks' shares of the tier check (tsb_peer_tier_verify) cover every owned unit once; the last rank decodes,
+    reading the source bytes, with the slot table after every token equal to the reference replay; every owned
+    unit's pulls took one stripe from each store."""
+    from tierstream_b200 import abi
+    monkeypatch.setenv("TSB_DG_DETERMINISTIC", "1")
+    m = model
+    ids = synth.zipf_trace(40, m.layers, m.units, 2, s=1.0, seed=22)
+    keys = m.layers * m.units
+    owner = peer.plan_owners(route_counts(m, ids[:10]), world,
+                             cap_units=[keys // (2 * world)] * world if mixed else None)
+    assert ((owner < 0).any()) == mixed
+    owned = int((owner >= 0).sum())
+    desc = runtime.Desc(m.desc())
+    stores = [peer.Store(desc, owner, r, 0, layout=abi.PEER_STRIPED, world=world) for r in range(world)]
+    stripe = peer.stripe_bytes(m.unit_bytes, world)
+    assert stripe == -(-(-(-m.unit_bytes // world)) // 256) * 256
+    assert all(s.bytes == owned * stripe for s in stores)
+    bases = [s.base for s in stores]
+    checked = [peer.verify_tier(desc, peer.Tier(world, r, owner, bases, copy, abi.PEER_STRIPED), 0)
+               for r in range(world)]
+    assert sum(checked) == owned and max(checked) - min(checked) <= 1
+    k0 = int(np.nonzero(owner >= 0)[0][0])
+    lo, n = peer.stripe_range(m.unit_bytes, world, world - 1)
+    assert np.array_equal(peer.read_device(stores[-1].base, n),
+                          m.unit_bytes_of(k0 // m.units, k0 % m.units)[lo:lo + n])
+    rank = world - 1
+    tier = peer.Tier(world, rank, owner, bases, copy=copy, layout=abi.PEER_STRIPED)
+    run = harness.DgRun(m, residents_per_layer=3, max_ids=2, verify=True, peer=tier)
+    try:
+        open_table = run.ctx.table(run.keys).copy()
+        t_ref, s_ref = oracle.ref_replay(replay_cfg_for(run, m, ids.shape[0]), ids)
+        check_run(run, m, ids, expected_sums(m, orc), t_ref)
+        st = run.ctx.stats()
+        assert st["misses"] == s_ref[-1][2] and st["fetched"] == s_ref[-1][4]
+        import json
+        pj = json.loads(run.ctx.stats_json())["peer"]
+        assert pj["layout"] == "striped" and pj["world"] == world and pj["self_units"] == 0
+        assert pj["peer_units"] > 0 and pj["self_bytes"] == pj["peer_units"] * n
+        assert pj["peer_bytes"] + pj["self_bytes"] == pj["peer_units"] * m.unit_bytes
+        if not mixed:
+            assert pj["peer_units"] == st["fetched"] + st["prefetched"]
+        run.ctx.check()
+        for L in range(m.layers):
+            for u in range(m.units):
+                run.ctx.check_unit(L, u)
+        run.ctx.reset_open()  # residents taken from the stores again, stripe by stripe
+        assert np.array_equal(run.ctx.table(run.keys), open_table)
+        for L in range(m.layers):
+            for u in range(m.units):
+                run.ctx.check_unit(L, u)
+    finally:
+        run.close()
+        for s in stores:
+            s.close()
+
+
+def test_striped_tier_check_finds_a_changed_byte(model):
+    """One byte of one stripe changed in its store: the share of the tier check that gathers that unit reports
+    SS_E_HASH, the other share passes; a striped store refuses a migration and a per-store check."""
+    from tierstream_b200 import abi
+    m = model
+    owner = peer.plan_owners(np.ones(m.layers * m.units, dtype=np.uint64), 2)
+    desc = runtime.Desc(m.desc())
+    stores = [peer.Store(desc, owner, r, 0, layout=abi.PEER_STRIPED, world=2) for r in range(2)]
+    bases = [s.base for s in stores]
+    try:
+        for r in range(2):
+            peer.verify_tier(desc, peer.Tier(2, r, owner, bases, 0, abi.PEER_STRIPED), 0)
+
+        class _View:  # stripe 1 of owned unit 0 (position 0: rank 0's share), byte 5
+            __cuda_array_interface__ = {"shape": (16,), "typestr": "|u1", "data": (bases[1], False), "version": 3}
+
+        v = torch.as_tensor(_View(), device="cuda")
+        v[5] ^= 0x5A
+        torch.cuda.synchronize()
+        with pytest.raises(abi.TsError) as e:
+            peer.verify_tier(desc, peer.Tier(2, 0, owner, bases, 0, abi.PEER_STRIPED), 0)
+        assert e.value.status == abi.SS_E_HASH
+        assert peer.verify_tier(desc, peer.Tier(2, 1, owner, bases, 0, abi.PEER_STRIPED), 0) > 0
+        s = torch.cuda.Stream()
+        dst = peer.Store(desc, owner, 0, 0, fill=False, layout=abi.PEER_STRIPED, world=2)
+        with pytest.raises(abi.TsError) as e:
+            dst.migrate_from(owner, bases, s.cuda_stream)
+        assert e.value.status == abi.SS_E_UNSUPPORTED
+        dst.close()
+    finally:
+        for s in stores:
+            s.close()
+
+
 def test_replan_migrates_the_stores_mid_decode(model, orc, monkeypatch):
     """A planning round between tokens: new owners from other counts, new stores filled from the current ones
     (tsb_peer_store_migrate), the context switched to them (tsb_dg_peer_retier), the old stores freed. The decode
@@ -141,7 +237,7 @@ def test_replan_migrates_the_stores_mid_decode(model, orc, monkeypatch):
             x.close()
 
 
-def _two_gpu_rank(rank, world, port, path, out_dir):
+def _two_gpu_rank(rank, world, port, path, out_dir, layout):
     import torch.distributed as dist
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
@@ -157,13 +253,16 @@ def _two_gpu_rank(rank, world, port, path, out_dir):
         ids = synth.zipf_trace(30, m.layers, m.units, 2, s=1.0, seed=40 + rank)
         desc = runtime.Desc(m.desc())
         setup = peer.PeerSetup(desc, route_counts(m, ids[:10]), dist, world, rank, rank, verify=True, copy=0,
-                               collective_device=torch.device("cuda", rank))
+                               collective_device=torch.device("cuda", rank), layout=layout)
+        if layout:  # striped: the ranks' shares of the tier check gathered every unit over NVLink
+            assert setup.checked_units == m.layers * m.units // world
         run = harness.DgRun(m, residents_per_layer=3, max_ids=2, peer=setup.tier)
         got = [run.step(ids[t]) for t in range(15)]
-        # a planning round mid-decode: other counts, new owners, stores migrated over NVLink, the context switched
+        # a planning round mid-decode: other counts, new owners, stores migrated over NVLink (striped: kept), the
+        # context switched
         mig = setup.replan(desc, route_counts(m, synth.zipf_trace(10, m.layers, m.units, 2, s=1.0, seed=70 + rank)),
                            dist, world, rank, rank, ctx=run.ctx, collective_device=torch.device("cuda", rank))
-        assert mig["units"] == (setup.owner == rank).sum()
+        assert mig["units"] == (0 if layout else (setup.owner == rank).sum())
         got += [run.step(ids[t]) for t in range(15, ids.shape[0])]
         got = np.stack(got)
         tables = np.stack([run.ctx.table(run.keys)])  # final table only; per-token parity is checked below
@@ -182,12 +281,14 @@ def _two_gpu_rank(rank, world, port, path, out_dir):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-def test_two_gpus_exchange_and_pull(model, orc, tmp_path):
+@pytest.mark.parametrize("layout", [0, 1], ids=["whole", "striped"])
+def test_two_gpus_exchange_and_pull(model, orc, tmp_path, layout):
     import torch.multiprocessing as mp
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
         port = s.getsockname()[1]
-    mp.start_processes(_two_gpu_rank, args=(2, port, model.path, str(tmp_path)), nprocs=2, start_method="spawn")
+    mp.start_processes(_two_gpu_rank, args=(2, port, model.path, str(tmp_path), layout), nprocs=2,
+                       start_method="spawn")
     want = expected_sums(model, orc)
     r = [np.load(tmp_path / ("r%d.npz" % i)) for i in range(2)]
     assert np.array_equal(r[0]["owner"], r[1]["owner"])

@@ -123,6 +123,47 @@ def test_open_peer_refuses_bad_tiers():
     assert opened(t) == abi.SS_E_INVALID
 
 
+def test_stripe_geometry():
+    """The striped layout's stripes: ceil(unit / world) rounded up to 256 bytes, covering the unit once in rank order,
+    the last ones shorter or empty; the benchmarked expert sizes cut into equal stripes."""
+    for unit, world in [(8192, 2), (8192, 3), (99090432, 8), (44040192, 8), (1000, 8), (100, 3), (256, 1)]:
+        s = peer.stripe_bytes(unit, world)
+        assert s % 256 == 0 and s * world >= unit and s - 256 < -(-unit // world)
+        ranges = [peer.stripe_range(unit, world, r) for r in range(world)]
+        assert sum(n for _, n in ranges) == unit
+        assert all(lo == r * s for r, (lo, _) in enumerate(ranges))
+        lens = [n for _, n in ranges]
+        assert lens == sorted(lens, reverse=True)  # full stripes, then at most one short one, then empty ones
+    assert peer.stripe_bytes(99090432, 8) == 99090432 // 8  # the Mixtral-shaped expert
+    assert peer.stripe_bytes(44040192, 8) == 44040192 // 8  # the DeepSeek-shaped expert
+    assert [peer.stripe_range(1000, 8, r)[1] for r in range(8)] == [256, 256, 256, 232, 0, 0, 0, 0]
+    assert abi.load().tsb_peer_stripe_bytes(1000, 0) == 0
+
+
+def test_striped_entry_points_refuse_bad_arguments():
+    m = synth.Model(os.path.join(harness.model_dir(), "tsb-peer-args.bin"), layers=2, units=4,
+                    part_bytes=(256, 256, 256), seed=1)
+    desc = runtime.Desc(m.desc())
+    lib = abi.load()
+    owner = np.zeros(8, dtype=np.int32)
+    op = owner.ctypes.data_as(C.POINTER(C.c_int32))
+    h = C.c_void_p()
+    assert lib.tsb_peer_store_create_striped(desc.h, op, 8, 2, 2, 0, 1, C.byref(h)) == abi.SS_E_INVALID
+    assert b"rank below it" in lib.ss_last_error()
+    assert lib.tsb_peer_store_create_striped(desc.h, op, 8, 0, 0, 0, 1, C.byref(h)) == abi.SS_E_INVALID
+    assert lib.tsb_peer_store_create_striped(desc.h, op, 7, 0, 2, 0, 1, C.byref(h)) == abi.SS_E_INVALID
+    assert lib.tsb_peer_store_create_striped(None, op, 8, 0, 2, 0, 1, C.byref(h)) == abi.SS_E_INVALID
+    t = peer.Tier(2, 0, owner, [0x1000, 0x2000], layout=2).struct()
+    assert lib.tsb_peer_tier_verify(desc.h, C.byref(t), 0, None) == abi.SS_E_INVALID
+    assert b"layout must be" in lib.ss_last_error()
+    b = abi.budget_defaults()
+    o = abi.options_defaults()
+    o.forward_mode = abi.SS_FORWARD_DEVICE_GATED
+    t = peer.Tier(2, 0, owner, [0x1000, 0], layout=abi.PEER_STRIPED).struct()  # rank 1 holds stripes, no store
+    assert lib.tsb_open_peer(desc.h, C.byref(b), None, C.byref(o), C.byref(t), C.byref(h)) == abi.SS_E_INVALID
+    assert b"holds a stripe" in lib.ss_last_error()
+
+
 def test_replan_entry_points_refuse_bad_arguments():
     lib = abi.load()
     t = peer.Tier(1, 0, np.zeros(4, dtype=np.int32), [0x1000]).struct()

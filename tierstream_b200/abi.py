@@ -166,7 +166,10 @@ class ss_dg_round_result(C.Structure):
 class tsb_peer_tier(C.Structure):
     """tsb_peer_tier (include/tierstream/tsb.h): the peer tier's owners and store addresses for tsb_open_peer."""
     _fields_ = [("struct_size", u32), ("world", u32), ("rank", C.c_int32), ("keys", u32),
-                ("owner", C.POINTER(C.c_int32)), ("store_base", C.POINTER(vp)), ("copy", u32), ("reserved", u32)]
+                ("owner", C.POINTER(C.c_int32)), ("store_base", C.POINTER(vp)), ("copy", u32), ("layout", u32)]
+
+
+PEER_WHOLE_UNITS, PEER_STRIPED = 0, 1
 
 
 PEER_HANDLE_BYTES = 64
@@ -262,6 +265,9 @@ _PROTOS = {
     "tsb_peer_index": (C.c_int, [P(C.c_int32), u32, u32, P(i64), P(u64)]),
     "tsb_peer_store_create": (C.c_int, [vp, P(C.c_int32), u32, C.c_int32, C.c_int, C.c_int, P(vp)]),
     "tsb_peer_store_alloc": (C.c_int, [vp, P(C.c_int32), u32, C.c_int32, C.c_int, P(vp)]),
+    "tsb_peer_stripe_bytes": (u64, [u64, u32]),
+    "tsb_peer_store_create_striped": (C.c_int, [vp, P(C.c_int32), u32, C.c_int32, u32, C.c_int, C.c_int, P(vp)]),
+    "tsb_peer_tier_verify": (C.c_int, [vp, P(tsb_peer_tier), C.c_int, P(u64)]),
     "tsb_peer_store_free": (None, [vp]),
     "tsb_peer_store_base": (vp, [vp]),
     "tsb_peer_store_bytes": (u64, [vp]),

@@ -813,9 +813,26 @@ ss_status tsb_peer_unmap(void* base) {
   return guard([&] { tsb::ipc_unmap(base); });
 }
 
+uint64_t tsb_peer_stripe_bytes(uint64_t unit_bytes, uint32_t world) {
+  return world ? tsb::stripe_bytes(unit_bytes, world) : 0;
+}
+
+ss_status tsb_peer_store_create_striped(const ss_desc* d, const int32_t* owner, uint32_t keys, int32_t rank,
+                                        uint32_t world, int device, int fill, tsb_peer_store** out) {
+  return guard([&] {
+    need(d && owner && out, "tsb_peer_store_create_striped: null argument");
+    *out = nullptr;
+    auto s = std::make_unique<tsb_peer_store>();
+    s->s = std::make_unique<tsb::PeerStore>(d->d, std::vector<int32_t>(owner, owner + keys), rank, device, false,
+                                            fill != 0, tsb::kStriped, world);
+    *out = s.release();
+  });
+}
+
 namespace {
-// A tsb_peer_tier checked and turned into the library's form (keys: the gated units of the descriptor).
-tsb::PeerTier tier_from(const tsb_peer_tier* peer, uint32_t keys) {
+// A tsb_peer_tier checked and turned into the library's form (keys: the gated units of the descriptor; unit_bytes:
+// theirs, for the stripe size, or 0 where the context already knows it).
+tsb::PeerTier tier_from(const tsb_peer_tier* peer, uint32_t keys, uint64_t unit_bytes) {
   tsb::PeerTier t;
   need(peer->struct_size >= sizeof(tsb_peer_tier), "tsb_peer_tier: struct_size is smaller than this build's");
   need(peer->world >= 1, "tsb_peer_tier: world must be >= 1");
@@ -825,17 +842,29 @@ tsb::PeerTier tier_from(const tsb_peer_tier* peer, uint32_t keys) {
   tsb::require(peer->keys == keys, SS_E_INVALID,
                "tsb_peer_tier: keys " + std::to_string(peer->keys) + " where the descriptor has " +
                    std::to_string(keys) + " gated units");
+  need(peer->layout <= 1, "tsb_peer_tier: layout must be 0 (whole units) or 1 (striped)");
   t.world = peer->world;
   t.rank = peer->rank;
   t.copy = int(peer->copy);
+  t.layout = peer->layout;
   t.owner.assign(peer->owner, peer->owner + peer->keys);
   std::vector<uint64_t> per;
-  t.index = tsb::store_index(t.owner, t.world, &per);
+  t.index = tsb::store_index(t.owner, t.world, &per);  // (checks every owner is a rank below world)
   for (uint32_t r = 0; r < peer->world; ++r) t.base.push_back(static_cast<char*>(peer->store_base[r]));
-  for (uint32_t r = 0; r < t.world; ++r)
-    tsb::require(!per[r] || t.base[r], SS_E_INVALID,
-                 "tsb_peer_tier: rank " + std::to_string(r) + " owns " + std::to_string(per[r]) +
-                     " units but its store_base is null");
+  if (t.layout == tsb::kStriped) {
+    uint64_t owned = 0;
+    t.index = tsb::striped_index(t.owner, &owned);
+    t.stripe = unit_bytes ? tsb::stripe_bytes(unit_bytes, t.world) : 0;
+    for (uint32_t r = 0; r < t.world && unit_bytes; ++r)
+      tsb::require(!owned || !tsb::stripe_len(unit_bytes, t.stripe, r) || t.base[r], SS_E_INVALID,
+                   "tsb_peer_tier: rank " + std::to_string(r) + " holds a stripe of " + std::to_string(owned) +
+                       " units but its store_base is null");
+  } else {
+    for (uint32_t r = 0; r < t.world; ++r)
+      tsb::require(!per[r] || t.base[r], SS_E_INVALID,
+                   "tsb_peer_tier: rank " + std::to_string(r) + " owns " + std::to_string(per[r]) +
+                       " units but its store_base is null");
+  }
   t.all_owned = std::all_of(t.owner.begin(), t.owner.end(), [](int32_t o) { return o >= 0; });
   return t;
 }
@@ -845,7 +874,7 @@ ss_status tsb_dg_peer_retier(ss_ctx* c, const tsb_peer_tier* peer) {
   return ctx_guard(c, [&] {
     need(peer != nullptr, "tsb_dg_peer_retier: null tier");
     auto& dg = dg_of(c, "tsb_dg_peer_retier");
-    dg.set_peer(tier_from(peer, peer->keys));
+    dg.set_peer(tier_from(peer, peer->keys, 0));
   });
 }
 
@@ -870,10 +899,20 @@ ss_status tsb_open_peer(const ss_desc* d, const ss_budget* budget, const ss_plan
   tsb::PeerTier t;
   const ss_status st = guard([&] {
     need(d && peer, "tsb_open_peer: null argument");
-    t = tier_from(peer, tsb::gated_keys(d->d).keys());
+    const tsb::GatedKeys gk = tsb::gated_keys(d->d);
+    t = tier_from(peer, gk.keys(), gk.unit_bytes);
   });
   if (st != SS_OK) return st;
   return open_impl(d, budget, plan, opt, &t, out);
+}
+
+ss_status tsb_peer_tier_verify(const ss_desc* d, const tsb_peer_tier* peer, int device, uint64_t* checked_units) {
+  return guard([&] {
+    need(d && peer, "tsb_peer_tier_verify: null argument");
+    const tsb::GatedKeys gk = tsb::gated_keys(d->d);
+    const uint64_t n = tsb::verify_tier(d->d, tier_from(peer, gk.keys(), gk.unit_bytes), device);
+    if (checked_units) *checked_units = n;
+  });
 }
 
 // ---- not in this build ----

@@ -5,7 +5,10 @@ all-reduce (NCCL on GPUs, gloo on CPU) -- the tier's only collective; every rank
 (tsb_peer_plan), fills its own store from the descriptor's sources (tsb_peer_store_create), and the ranks exchange
 their stores' CUDA IPC handles (an all-gather of 64-byte handles) and map each other's stores. A device-gated context
 opened with the resulting Tier (runtime.DgContext(..., peer=tier)) copies each miss on an owned unit from its owner's
-store: over NVLink for a peer, inside HBM for its own.
+store: over NVLink for a peer, inside HBM for its own. With layout=abi.PEER_STRIPED every rank's store holds one
+stripe of every owned unit instead (tsb_peer_store_create_striped), a miss reads a stripe from each GPU, and the
+stores are checked against the descriptor's hashes once mapped (tsb_peer_tier_verify), each rank gathering its share
+of the units.
 """
 import ctypes as C
 
@@ -39,15 +42,33 @@ def store_index(owner, world):
     return index, per
 
 
-class Store:
-    """This rank's store: the units it owns, in its GPU's HBM (tsb_peer_store_create)."""
+def stripe_bytes(unit_bytes, world):
+    """The striped layout's stripe size (tsb_peer_stripe_bytes)."""
+    return int(abi.load().tsb_peer_stripe_bytes(unit_bytes, world))
 
-    def __init__(self, desc, owner, rank, device=0, verify=True, fill=True):
-        """fill = False: allocated only (tsb_peer_store_alloc); the caller writes every unit."""
+
+def stripe_range(unit_bytes, world, r):
+    """(offset, bytes) of stripe r of a unit in the striped layout."""
+    s = stripe_bytes(unit_bytes, world)
+    lo = r * s
+    return lo, max(0, min(s, unit_bytes - lo))
+
+
+class Store:
+    """This rank's store: the units it owns, in its GPU's HBM (tsb_peer_store_create), or with
+    layout=abi.PEER_STRIPED its stripe of every owned unit (tsb_peer_store_create_striped)."""
+
+    def __init__(self, desc, owner, rank, device=0, verify=True, fill=True, layout=abi.PEER_WHOLE_UNITS, world=1):
+        """fill = False: allocated only (tsb_peer_store_alloc); the caller writes every unit (or stripe). A striped
+        store is never checked here (verify ignored): check the tier once mapped (verify_tier)."""
         owner = np.ascontiguousarray(owner, dtype=np.int32)
         self.h = C.c_void_p()
+        self.layout = layout
         op = owner.ctypes.data_as(C.POINTER(C.c_int32))
-        if fill:
+        if layout == abi.PEER_STRIPED:
+            abi.check(abi.load().tsb_peer_store_create_striped(desc.h, op, owner.size, rank, world, device,
+                                                               1 if fill else 0, C.byref(self.h)))
+        elif fill:
             abi.check(abi.load().tsb_peer_store_create(desc.h, op, owner.size, rank, device, 1 if verify else 0,
                                                        C.byref(self.h)))
         else:
@@ -111,8 +132,8 @@ def unmap_store(base):
 class Tier:
     """The owners and each rank's store address as seen from this process: the tsb_peer_tier of tsb_open_peer."""
 
-    def __init__(self, world, rank, owner, bases, copy=0):
-        self.world, self.rank, self.copy = world, rank, copy
+    def __init__(self, world, rank, owner, bases, copy=0, layout=abi.PEER_WHOLE_UNITS):
+        self.world, self.rank, self.copy, self.layout = world, rank, copy, layout
         self.owner = np.ascontiguousarray(owner, dtype=np.int32)
         self.bases = (C.c_void_p * world)(*[b or None for b in bases])
 
@@ -123,7 +144,17 @@ class Tier:
         t.owner = self.owner.ctypes.data_as(C.POINTER(C.c_int32))
         t.store_base = C.cast(self.bases, C.POINTER(C.c_void_p))
         t.copy = self.copy
+        t.layout = self.layout
         return t
+
+
+def verify_tier(desc, tier, device):
+    """This rank's share of the tier checked against the descriptor's hashes (tsb_peer_tier_verify): the units
+    checked; raises on a mismatch."""
+    t = tier.struct()
+    n = C.c_uint64()
+    abi.check(abi.load().tsb_peer_tier_verify(desc.h, C.byref(t), device, C.byref(n)))
+    return n.value
 
 
 def all_reduce_counts(counts, dist, device=None):
@@ -151,15 +182,19 @@ class PeerSetup:
     Close it after the context that uses it."""
 
     def __init__(self, desc, local_counts, dist, world, rank, device, cap_units=None, verify=True, copy=0,
-                 collective_device=None, filler=None):
-        """filler(store, owner): writes the rank's store itself (the store is then only allocated by the library)."""
+                 collective_device=None, filler=None, layout=abi.PEER_WHOLE_UNITS):
+        """filler(store, owner): writes the rank's store itself (the store is then only allocated by the library).
+        layout=abi.PEER_STRIPED: striped stores; with verify, every rank checks its share of the units once all
+        stores are mapped (tsb_peer_tier_verify), before the closing barrier."""
         if dist is None:  # one rank: nothing to exchange
             assert world == 1 and rank == 0
             self.counts = np.ascontiguousarray(local_counts, dtype=np.uint64)
         else:
             self.counts = all_reduce_counts(local_counts, dist, collective_device)
         self.owner = plan_owners(self.counts, world, cap_units)
-        self.store = Store(desc, self.owner, rank, device, verify, fill=filler is None)
+        self.layout = layout
+        self.checked_units = 0
+        self.store = Store(desc, self.owner, rank, device, verify, fill=filler is None, layout=layout, world=world)
         if filler is not None:
             filler(self.store, self.owner)
         handles = ([self.store.handle()] if dist is None else
@@ -173,7 +208,11 @@ class PeerSetup:
                 b = map_store(handles[r], device)
                 self.mapped.append(b)
                 bases.append(b)
-        self.tier = Tier(world, rank, self.owner, bases, copy)
+        self.tier = Tier(world, rank, self.owner, bases, copy, layout)
+        if layout == abi.PEER_STRIPED and verify:
+            if dist is not None:
+                dist.barrier()  # every store written before any rank gathers from it
+            self.checked_units = verify_tier(desc, self.tier, device)
         if dist is not None:
             dist.barrier()
 
@@ -187,6 +226,16 @@ class PeerSetup:
         import torch
         counts = local_counts if dist is None else all_reduce_counts(local_counts, dist, collective_device)
         new_owner = plan_owners(counts, world, cap_units)
+        if self.layout == abi.PEER_STRIPED:
+            # striped stores do not depend on the owners: the same owned units keep the same stores
+            if not np.array_equal(new_owner >= 0, self.owner >= 0):
+                raise ValueError("a striped tier's re-plan must keep the same owned units")
+            tier = Tier(world, rank, new_owner, [self.tier.bases[r] for r in range(world)], self.tier.copy,
+                        self.layout)
+            if ctx is not None:
+                ctx.retier(tier)
+            self.tier, self.owner, self.counts = tier, new_owner, counts
+            return {"units": 0, "peer_units": 0, "bytes": 0, "seconds": 0.0}
         old_owner, old_bases = self.owner, [self.tier.bases[r] for r in range(world)]
         store = Store(desc, new_owner, rank, device, verify=False, fill=False)
         s = torch.cuda.Stream(device=device)
