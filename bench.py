@@ -105,14 +105,18 @@ def args_():
     p.add_argument("--layers", type=int, default=0,
                    help="qwen3 / deepseek only: fewer layers than the config's, for fewer GPUs (the "
                         "line then names the layer count; not the config's number)")
-    p.add_argument("--peer-layout", default="whole", choices=["whole", "striped"],
-                   help="peer tier stores: whole units at their owners, or every unit striped over all GPUs (a miss "
-                        "reads a stripe from each)")
+    p.add_argument("--peer-layout", default="auto", choices=["auto", "whole", "striped"],
+                   help="peer tier stores: whole units at their owners, every unit striped over all GPUs (a miss "
+                        "reads a stripe from each), or auto (the default): striped for the Mixtral shape (1,959 "
+                        "against 1,723 GB/s for whole units at 4 GPUs, 1,222 against 1,156 at 2), whole units for the "
+                        "top-8 shapes (measured that way)")
     p.add_argument("--peer-copy", default="auto", choices=["auto", "kernel", "ce"],
                    help="peer tier mover: the copy engines, the land kernel's SM loads, or auto (the default): the "
-                        "copy engines for the Mixtral shape (one or two misses a layer: 2,950 against 2,751 GB/s at "
-                        "8 GPUs, 1,734 against 1,673 at 4), the land kernel for the top-8 shapes (several owners' units "
-                        "a layer pulled at once: 2,161 against 1,886 GB/s for DeepSeek at 4 GPUs)")
+                        "land kernel for striped stores (it pulls every stripe at once; one copy-engine stream takes "
+                        "them in turn: 1,611 GB/s at 4 GPUs); for whole units the copy engines for the Mixtral shape "
+                        "(one or two misses a layer: 2,950 against 2,751 GB/s at 8 GPUs) and the land kernel for the "
+                        "top-8 shapes (several owners' units a layer pulled at once: 2,161 against 1,886 GB/s for "
+                        "DeepSeek at 4 GPUs)")
     return p.parse_args()
 
 
@@ -129,9 +133,12 @@ def model_path():
 
 
 def configure(a):
-    """Sets the workload's shape (the module constants) and resolves --peer-copy auto."""
+    """Sets the workload's shape (the module constants) and resolves --peer-layout and --peer-copy auto."""
+    mixtral = a.workload == "mixtral-8x7b-dg"
+    if a.peer_layout == "auto":
+        a.peer_layout = "striped" if mixtral else "whole"
     if a.peer_copy == "auto":
-        a.peer_copy = "ce" if a.workload == "mixtral-8x7b-dg" else "kernel"
+        a.peer_copy = "ce" if mixtral and a.peer_layout == "whole" else "kernel"
     shapes = {"qwen3-235b-a22b-peer": (QWEN3, 8), "deepseek-v3-peer": (DEEPSEEK, 12)}
     if a.workload in shapes:
         shape, per_layer = shapes[a.workload]

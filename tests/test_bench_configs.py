@@ -59,3 +59,24 @@ def test_reference_cuda_directory_holds_what_the_driver_reads(tmp_path, monkeypa
     finally:
         import shutil
         shutil.rmtree(d, ignore_errors=True)
+
+
+def test_peer_defaults_follow_the_measurements(monkeypatch):
+    """--peer-layout / --peer-copy auto: striped stores with the land kernel for the Mixtral shape, whole units with
+    the land kernel for the top-8 shapes, the copy engines for Mixtral's whole units; explicit choices kept."""
+    sys.path.insert(0, ROOT)
+    import bench
+    cases = [([], ("striped", "kernel")), (["--workload", "deepseek-v3-peer"], ("whole", "kernel")),
+             (["--workload", "qwen3-235b-a22b-peer"], ("whole", "kernel")), (["--peer-layout", "whole"], ("whole", "ce")),
+             (["--peer-layout", "striped", "--peer-copy", "ce"], ("striped", "ce"))]
+    for argv, want in cases:
+        monkeypatch.setattr(sys, "argv", ["bench.py"] + argv)
+        a = bench.args_()
+        names = set(bench.QWEN3) | set(bench.DEEPSEEK) | {"LAYERS", "RESIDENTS", "MODEL_FILE"}
+        saved = {k: getattr(bench, k) for k in names if hasattr(bench, k)}  # configure sets the module's shape
+        try:
+            bench.configure(a)
+        finally:
+            for k, v in saved.items():
+                setattr(bench, k, v)
+        assert (a.peer_layout, a.peer_copy) == want, argv
