@@ -86,8 +86,8 @@ typedef struct tsb_dg_replay_config {
   const uint8_t* disk;
   uint64_t* xstats;
   /* reset_at (0 = never): ss_dg_reset_open after the boundary of token reset_at - 1, before that token's table and
-   * counters are recorded (the open placement restored, moving only misplaced units) */
-  uint32_t reset_at, reserved;
+   * counters are recorded (the open placement restored, moving only misplaced units); bank_keep: dg_bank_keep (0..2) */
+  uint32_t reset_at, bank_keep;
   /* scored eviction: policy 0 LRU, 1 SCORED, 2 SCORED_AUTO; rows = each token's row count at its boundary (0 = 1);
    * weights out of 1000 (all 0 = 700 / 200 / 100); profile (optional): per gated layer units^2 transition counts,
    * row-major [previous unit][unit], loaded as the open state */
@@ -121,6 +121,9 @@ typedef struct tsb_dg_replay_config {
   uint64_t* mstats;
   /* sstats (optional): [tokens][5] score_fallbacks, scored_victims, score_layers, score_candidates, score_saturated */
   uint64_t* sstats;
+  /* kstats (optional): [tokens][4] bank_kept, bank_keep_drops, bank_keep_rereads, and the FNV-1a 64 hash of the
+   * pinned homes' recency order (gated keys as 4 little-endian bytes each, most recently homed first) */
+  uint64_t* kstats;
 } tsb_dg_replay_config;
 SS_API ss_status tsb_test_dg_replay(const tsb_dg_replay_config* cfg, const int32_t* ids, const int32_t* preds,
                                     int32_t* tables, uint64_t* stats, const uint8_t* src_units, uint64_t* read_sum);

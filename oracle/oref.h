@@ -31,7 +31,8 @@ typedef struct oref_dg_config {
   uint32_t disk_tier, disk_prefetch, home_blocks, disk_staging;
   const uint8_t* disk;
   uint64_t* xstats;
-  uint32_t reset_at, reserved;  /* reset_at (0 = never): reset_open after the boundary of token reset_at - 1 */
+  uint32_t reset_at, bank_keep; /* reset_at (0 = never): reset_open after the boundary of token reset_at - 1;
+                                   bank_keep: dg_bank_keep (0..2) */
   /* scored eviction: policy 0 LRU / 1 SCORED / 2 SCORED_AUTO, rows per boundary (0 = 1), weights out of 1000 (all 0 =
    * the defaults), profile (optional): per gated layer units^2 counts, loaded through a TSSCPRF1 profile */
   uint32_t policy, rows;
@@ -61,6 +62,9 @@ typedef struct oref_dg_config {
   uint64_t* mstats;
   /* sstats (optional): [tokens][5] score_fallbacks, scored_victims, score_layers, score_candidates, score_saturated */
   uint64_t* sstats;
+  /* kstats (optional): [tokens][4] bank_kept, bank_keep_drops, bank_keep_rereads, FNV-1a 64 of the pinned homes'
+   * recency order (keys as 4 little-endian bytes, most recently homed first) */
+  uint64_t* kstats;
 } oref_dg_config;
 #define OREF_NXSTATS 6
 

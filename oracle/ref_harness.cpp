@@ -150,6 +150,7 @@ extern "C" __attribute__((visibility("default"))) int oref_dg_replay(const oref_
     cfg.clean_evict = c->clean_evict != 0;
     cfg.pf_revert = c->pf_revert != 0;
     cfg.pf_strict = c->pf_strict != 0;
+    cfg.bank_keep = c->bank_keep;
     if (c->w_trans || c->w_freq || c->w_rec) {
       cfg.w_trans = c->w_trans;
       cfg.w_freq = c->w_freq;
@@ -278,6 +279,14 @@ extern "C" __attribute__((visibility("default"))) int oref_dg_replay(const oref_
         const uint64_t pv[5] = {q.clean_drops, q.clean_drop_bytes, q.pf_reverted, q.pf_revert_bytes,
                                 q.pf_strict_refused};
         std::memcpy(c->pstats + size_t(tok) * 5, pv, sizeof pv);
+      }
+      if (c->kstats) {  // FNV-1a 64 of the pinned recency order, each key's 4 little-endian bytes
+        const ts::DgStats& q = core.stats();
+        uint64_t h = 0xcbf29ce484222325ull;
+        for (uint32_t k : core.host_order())
+          for (int b = 0; b < 4; ++b) h = (h ^ ((k >> (8 * b)) & 0xffu)) * 0x100000001b3ull;
+        const uint64_t kv[4] = {q.bank_kept, q.bank_keep_drops, q.bank_keep_rereads, h};
+        std::memcpy(c->kstats + size_t(tok) * 4, kv, sizeof kv);
       }
       std::memcpy(tables + size_t(tok) * keys, t.table_.data(), size_t(keys) * 4);
       const ts::DgStats& s = core.stats();

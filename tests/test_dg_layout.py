@@ -1,8 +1,8 @@
 """The device-gated layout ss_open takes (slots, banks, blocks, spare and file units, staging buffers, the resolved
 read depth and score weights, the residents) against the reference's own dg_layout on the same descriptor, tiers,
 budget and options, on the CPU: every number is identical, or both refuse with the same status. Options this build
-refuses as unsupported (landings, bank keep, adaptive depth, priors) are left out; host read-ahead, which both refuse
-with SS_E_INVALID in this mode, is tests/test_open_refusals.py's."""
+refuses as unsupported (landings, adaptive depth, priors) are left out; host read-ahead, which both refuse with
+SS_E_INVALID in this mode, is tests/test_open_refusals.py's."""
 import ctypes as C
 import os
 
@@ -87,6 +87,8 @@ def random_case(seed, tmp):
     for f in ("dg_no_admit", "dg_clean_evict", "dg_pf_revert_unused", "dg_pf_strict_admit"):
         if r.random() < 0.15:
             setattr(o, f, 1)
+    if r.random() < 0.2:
+        o.dg_bank_keep = int(r.integers(1, 3))
     return desc_json, tiers, b, o
 
 
@@ -101,6 +103,23 @@ def test_layout_matches_reference(ref, tmp_path, seed):
     if st == abi.SS_OK:
         assert np.array_equal(out, r_out), "layout %s vs %s" % (out.tolist(), r_out.tolist())
         assert np.array_equal(res, r_res)
+
+
+def test_bank_keep_values(ref, tmp_path):
+    """dg_bank_keep 0, 1 and 2 open (the same layout as the reference's); 3 is refused by both with SS_E_INVALID."""
+    for seed in range(150):
+        desc_json, tiers, b, o = random_case(seed, str(tmp_path))
+        st, _, _ = ours(desc_json, tiers, b, o)
+        if st == abi.SS_OK:
+            break
+    for v, want in ((0, abi.SS_OK), (1, abi.SS_OK), (2, abi.SS_OK), (3, abi.SS_E_INVALID)):
+        o.dg_bank_keep = v
+        st, out, _ = ours(desc_json, tiers, b, o)
+        r_st, r_out, _, r_err = reference(desc_json, tiers, b, o)
+        assert st == r_st == want, (v, st, r_st, r_err)
+        if st == abi.SS_OK:
+            assert np.array_equal(out, r_out)
+    assert b"dg_bank_keep" in abi.load().ss_last_error()
 
 
 def test_layout_cases_are_mostly_accepted(ref, tmp_path):

@@ -411,6 +411,43 @@ def test_file_tier_bytes_and_tables_match_reference(small_model, orc, ref, monke
         run.close()
 
 
+@pytest.mark.parametrize("bank_keep", [1, 2])
+def test_file_tier_bank_keep_matches_reference(small_model, orc, ref, monkeypatch, bank_keep):
+    """dg_bank_keep: a bank-served file miss is read (and hashed) straight into a pinned block, which becomes its home
+    when the bank lets it go (1: at the pinned recency front, 2: behind its front half), dropping the least recently
+    homed pinned unit to its file when no block is free. Every routed unit's bytes are the source's; the slot table,
+    the file counters and the option's counters after every token equal the reference DgCore's replay; every unit's
+    live copy (a kept block included) holds its bytes at the end."""
+    import json
+    monkeypatch.setenv("TSB_DG_DETERMINISTIC", "1")
+    m = small_model
+    ids = synth.zipf_trace(40, m.layers, m.units, 2, s=0.8, seed=21)
+    run, res, disk = file_tier_run(m, S=3, verify=True, bank_keep=bank_keep)
+    try:
+        cfg = file_tier_cfg(run, m, res, disk, ids, 3, bank_keep=bank_keep)
+        x_ref = np.zeros((ids.shape[0], 6), dtype=np.uint64)
+        k_ref = np.zeros((ids.shape[0], 4), dtype=np.uint64)
+        t_ref, s_ref = oracle.ref_replay(cfg, ids, xstats=x_ref, kstats=k_ref)
+        want = expected_sums(m, orc)
+        for t in range(ids.shape[0]):
+            got = run.step(ids[t])
+            keys = np.arange(m.layers)[:, None] * m.units + ids[t]
+            assert np.array_equal(got, want[keys]), "token %d read wrong bytes" % t
+            assert np.array_equal(run.ctx.table(run.keys), t_ref[t]), "slot table differs after token %d" % t
+        st = run.ctx.stats()
+        assert st["misses"] == s_ref[-1][2] and st["bank_serves"] == s_ref[-1][8] > 0
+        assert st["disk_reads"] == x_ref[-1][0] and st["disk_drops"] == x_ref[-1][3]
+        dj = json.loads(run.ctx.stats_json())["dg"]  # (bank_kept: ss_dg_stats.bank_kept)
+        assert dj["bank_keep"] == bank_keep and dj["bank_kept"] == k_ref[-1][0] > 0
+        assert dj["bank_keep_drops"] == k_ref[-1][1] > 0 and dj["bank_keep_rereads"] == k_ref[-1][2]
+        run.ctx.check()
+        for L in range(m.layers):
+            for u in range(m.units):
+                run.ctx.check_unit(L, u)
+    finally:
+        run.close()
+
+
 def test_file_tier_predictions_read_files(small_model, orc, ref, monkeypatch):
     """dg_disk_prefetch: predictions read file units too (on the prefetch stream, covered by the demand's wait)."""
     monkeypatch.setenv("TSB_DG_DETERMINISTIC", "1")

@@ -141,7 +141,7 @@ class dg_replay_config(C.Structure):
                 ("n_order", u32), ("order", C.POINTER(u32)), ("tokens", u32), ("n_ids", u32), ("n_pred", u32),
                 ("move_bytes", u32), ("inclusive", u32), ("disk_tier", u32), ("disk_prefetch", u32),
                 ("home_blocks", u32), ("disk_staging", u32), ("disk", C.POINTER(C.c_uint8)),
-                ("xstats", C.POINTER(u64)), ("reset_at", u32), ("reserved", u32), ("policy", u32), ("rows", u32),
+                ("xstats", C.POINTER(u64)), ("reset_at", u32), ("bank_keep", u32), ("policy", u32), ("rows", u32),
                 ("w_trans", u32), ("w_freq", u32), ("w_rec", u32), ("reserved2", u32),
                 ("profile", C.POINTER(u32)), ("round_every", u32), ("round_max_units", u32),
                 ("round_hysteresis", C.c_float), ("round_decay", C.c_float), ("round_budget", u64),
@@ -149,7 +149,7 @@ class dg_replay_config(C.Structure):
                 ("pf_strict", u32), ("pstats", C.POINTER(u64)), ("disk_queue", u32), ("reserved3", u32),
                 ("qstats", C.POINTER(u64)), ("mr_n", u32), ("reserved4", u32), ("mr_token", C.POINTER(u32)),
                 ("mr_layer", C.POINTER(u32)), ("mr_count", C.POINTER(u32)), ("mr_ids", C.POINTER(u32)),
-                ("mstats", C.POINTER(u64)), ("sstats", C.POINTER(u64))]
+                ("mstats", C.POINTER(u64)), ("sstats", C.POINTER(u64)), ("kstats", C.POINTER(u64))]
 
 
 class ss_dg_round_params(C.Structure):

@@ -137,9 +137,10 @@ void SlotCache::leave_device(uint32_t k) {
   set_entry(k, -1);
 }
 
-void SlotCache::home_push(uint32_t k, bool cold) {
+void SlotCache::home_push(uint32_t k, bool cold, bool mid) {
   if (!c_.disk_tier) return;
   if (cold) homes_.push_back(k);  // the least recently homed: the first to drop to its file
+  else if (mid) homes_.push_behind_front_half(k);
   else homes_.push_front(k);
 }
 
@@ -317,7 +318,8 @@ void SlotCache::to_lower(uint32_t k, bool cold) {
     return;
   }
   x.home = Home::Host;
-  home_push(k, cold);
+  home_push(k, cold, x.keep_mid);
+  x.keep_mid = false;
 }
 
 // The least recently homed pinned unit (not skipped) goes to its file (no copy: the file holds its bytes); its block
@@ -336,6 +338,17 @@ bool SlotCache::drop_host_lru(const std::vector<uint8_t>* skip, bool count) {
   ++on_file_;
   st_.disk_drops += count ? 1 : 0;
   return true;
+}
+
+int32_t SlotCache::keep_block() {
+  if (!c_.bank_keep || !c_.disk_tier || c_.no_admit) return -1;
+  if (free_blocks_.empty()) {
+    const uint32_t oldest = homes_.back();
+    if (!drop_host_lru()) return -1;
+    e_[oldest].keep_drop = st_.tokens + 1;
+    ++st_.bank_keep_drops;
+  }
+  return free_blocks_.take();
 }
 
 // The next staging buffer in rotation, once a read still holding it ended and its last copy landed.
@@ -432,9 +445,11 @@ void SlotCache::finish_pending(const Pending& p) {
   if (mut_ == kEntryBeforeCopy) publish(p.s, p.key, p.slot);  // test-only fault: the entry before its bytes
   m_->h2d(p.s, p.slot, p.stage, p.key);
   if (mut_ != kEntryBeforeCopy) publish(p.s, p.key, p.slot);
-  void*& stage_ev = stage_ev_[uint32_t(p.stage) - c_.blocks];  // the buffer is reusable once this copy landed
-  if (stage_ev == nullptr) stage_ev = event();
-  m_->record(stage_ev, p.s);
+  if (uint32_t(p.stage) >= c_.blocks) {  // (a kept read's block is its key's own, not a staging buffer)
+    void*& stage_ev = stage_ev_[uint32_t(p.stage) - c_.blocks];  // the buffer is reusable once this copy landed
+    if (stage_ev == nullptr) stage_ev = event();
+    m_->record(stage_ev, p.s);
+  }
   if (!p.prefetch) return;
   Entry& x = e_[p.key];
   x.pf_done = event();
@@ -452,6 +467,12 @@ void SlotCache::undo_pending(const Pending& p) {
     banked_.erase(std::find(banked_.begin(), banked_.end(), p.key));
     --st_.bank_serves;
     --lc_[g].bank_serves;
+    if (x.block >= 0) {  // a kept read's block: never a home, free again
+      free_blocks_.give(x.block);
+      x.block = -1;
+      x.keep_mid = false;
+      --st_.bank_kept;
+    }
   } else {
     leave_device(p.key);
     coming_.erase(std::find(coming_.begin(), coming_.end(), p.key));
@@ -702,9 +723,11 @@ bool SlotCache::fetch(uint32_t g, uint32_t unit, bool prefetch) {
   const Mover::Stream s = prefetch ? Mover::kPf : Mover::kDem;
   const bool from_file = x.home == Home::File;
   if (from_file) {  // its bytes from the file into a staging buffer, then the same copy once the read ended
+    int32_t stage = -1;
     try {
       make_room_for_read();
-      const int32_t stage = take_stage();
+      stage = bank ? keep_block() : -1;  // bank_keep: into the pinned block that becomes its home
+      if (stage < 0) stage = take_stage();
       const auto t0 = Clock::now();
       void* handle = m_->read_begin(k, stage);
       st_.disk_read_ns += ns_since(t0);
@@ -716,10 +739,20 @@ bool SlotCache::fetch(uint32_t g, uint32_t unit, bool prefetch) {
         free_slots_.give(slot);
         demand_free_used_ -= free_counted ? 1 : 0;
       }
+      if (stage >= 0 && uint32_t(stage) < c_.blocks) free_blocks_.give(stage);  // (a kept read's block)
       throw;
+    }
+    if (uint32_t(stage) < c_.blocks) {  // kept: the block is the unit's own, its home once the bank lets it go
+      x.block = stage;
+      x.keep_mid = c_.bank_keep == 2;
+      ++st_.bank_kept;
     }
     set_entry(k, slot);  // the mirror now; the device's entry with the copy
     --on_file_;
+    if (x.keep_drop) {  // dropped to its file for a kept read: read back within 8 tokens counts as churn
+      st_.bank_keep_rereads += st_.tokens + 1 - x.keep_drop <= 8 ? 1 : 0;
+      x.keep_drop = 0;
+    }
   } else {
     if (mut_ == kEntryBeforeCopy) publish(s, k, slot);  // test-only fault: the entry before its bytes
     m_->h2d(s, slot, x.block, k);

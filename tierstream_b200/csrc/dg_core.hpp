@@ -134,6 +134,12 @@ struct CacheConfig {
   // unused prefetch goes back at the boundary (to its block at the pinned recency tail, or its file), not admitted;
   // pf_strict = a prefetch also leaves the spare target's slots free.
   bool no_admit = false, clean_evict = false, pf_revert = false, pf_strict = false;
+  // bank_keep (file tier; no effect with no_admit): a demand file miss served through a bank slot is read into a
+  // pinned block (a free one, else the least recently homed pinned unit's, that unit going to its file) instead of a
+  // staging buffer, and that block is its pinned home once the bank lets it go: at the front of the pinned recency
+  // list (1), or after its front half (2), so that a unit read once does not push out the most recently homed ones
+  // (dg_core.cpp:237-250, 1286-1303, 142-160, 200-213).
+  uint32_t bank_keep = 0;
 };
 
 struct CacheStats {
@@ -161,6 +167,9 @@ struct CacheStats {
   // opt-in policies: victims dropped to their file by clean_evict and their bytes; unused prefetches reverted and
   // their bytes; prefetches pf_strict refused
   uint64_t clean_drops = 0, clean_drop_bytes = 0, pf_reverted = 0, pf_revert_bytes = 0, pf_strict_refused = 0;
+  // bank_keep: file reads kept in a pinned block; pinned units dropped to their file for one; of those, the ones read
+  // back from their file within 8 tokens
+  uint64_t bank_kept = 0, bank_keep_drops = 0, bank_keep_rereads = 0;
   // make_resident: units copied in and evicted, bytes copied in, host time; its file reads, their bytes and time,
   // its write-back bytes
   uint64_t resident_units = 0, resident_evicted = 0, resident_bytes = 0, resident_ns = 0;
@@ -307,6 +316,7 @@ class SlotCache {
     uint32_t newer(uint32_t k) const { return link_[k].prev; }  // toward the front
     void push_front(uint32_t k) { insert(k, kNil, front_); }
     void push_back(uint32_t k) { insert(k, back_, kNil); }
+    void insert_behind(uint32_t at, uint32_t k) { insert(k, at, link_[at].next); }  // just older than `at`
     void erase(uint32_t k) {
       Link& l = link_[k];
       (l.prev == kNil ? front_ : link_[l.prev].next) = l.next;
@@ -326,6 +336,68 @@ class SlotCache {
     }
     std::vector<Link> link_;
     uint32_t front_ = kNil, back_ = kNil;
+  };
+  // The pinned homes, front = most recently homed, with a cursor on the oldest unit of the front half (its size / 2
+  // newest units) kept through every change, so a unit can enter right behind that half in O(1) (bank_keep 2).
+  class HomeList {
+   public:
+    void reset(uint32_t keys) {
+      list_.reset(keys);
+      in_front_.assign(keys, 0);
+      edge_ = kNil;
+      size_ = front_n_ = 0;
+    }
+    bool has(uint32_t k) const { return list_.has(k); }
+    uint32_t front() const { return list_.front(); }
+    uint32_t back() const { return list_.back(); }
+    uint32_t older(uint32_t k) const { return list_.older(k); }
+    uint32_t newer(uint32_t k) const { return list_.newer(k); }
+    void push_front(uint32_t k) {
+      list_.push_front(k);
+      in_front_[k] = 1;
+      ++front_n_;
+      if (edge_ == kNil) edge_ = k;
+      grew();
+    }
+    void push_back(uint32_t k) {
+      list_.push_back(k);
+      grew();
+    }
+    void push_behind_front_half(uint32_t k) {
+      if (edge_ == kNil) list_.push_front(k);
+      else list_.insert_behind(edge_, k);
+      grew();
+    }
+    void erase(uint32_t k) {
+      if (in_front_[k]) {
+        in_front_[k] = 0;
+        --front_n_;
+        if (edge_ == k) edge_ = list_.newer(k);
+      }
+      list_.erase(k);
+      --size_;
+      settle();
+    }
+
+   private:
+    void grew() {
+      ++size_;
+      settle();
+    }
+    // the front half back to size / 2 units: one step per change at most
+    void settle() {
+      for (; front_n_ > size_ / 2; --front_n_) {
+        in_front_[edge_] = 0;
+        edge_ = list_.newer(edge_);
+      }
+      for (; front_n_ < size_ / 2; ++front_n_) {
+        edge_ = edge_ == kNil ? list_.front() : list_.older(edge_);
+        in_front_[edge_] = 1;
+      }
+    }
+    KeyList list_;
+    std::vector<uint8_t> in_front_;
+    uint32_t edge_ = kNil, size_ = 0, front_n_ = 0;
   };
   // Free slots or blocks: a stack whose next is the one returned last (at open, the lowest index).
   class LifoPool {
@@ -353,6 +425,8 @@ class SlotCache {
     int32_t slot = -1, block = -1;
     bool wb_pending = false, via_pf = false, used = false;
     bool backed = false;  // a device unit whose block still holds its bytes (inclusive share)
+    bool keep_mid = false;  // bank_keep 2: a kept read, homed behind the pinned list's front half when released
+    uint64_t keep_drop = 0;  // bank_keep: tokens + 1 when dropped to its file for a kept read (0: not)
     uint64_t demand_epoch = 0, lru_stamp = 0;  // scored: the last token that routed it; its recency list position
     void* pf_done = nullptr;
   };
@@ -375,7 +449,8 @@ class SlotCache {
     std::vector<Entry> ent;
     std::vector<int32_t> table;
     LifoPool slots, blocks;
-    KeyList recent, homes;
+    KeyList recent;
+    HomeList homes;
     uint32_t on_device = 0, on_file = 0;
     uint64_t stamp = 0;
   };
@@ -383,7 +458,8 @@ class SlotCache {
   // ---- the recency list and the pinned homes' list ----
   void touch(uint32_t k);          // to the recency front (a fresh stamp when scored)
   void leave_device(uint32_t k);   // out of the recency list, entry withdrawn
-  void home_push(uint32_t k, bool cold = false);  // file tier: a pinned home, most (cold: least) recently homed
+  // file tier: a pinned home, most (cold: least) recently homed, or (mid) behind the front half of the list
+  void home_push(uint32_t k, bool cold = false, bool mid = false);
   void home_erase(uint32_t k);
   void recycle(void*& ev);         // an event back to the pool
   void count_fetch(uint32_t g, bool prefetch, int delta = 1);
@@ -455,6 +531,7 @@ class SlotCache {
   }
   // the least recently homed pinned unit not in `skip` to its file; count: a disk drop of the boundary
   bool drop_host_lru(const std::vector<uint8_t>* skip = nullptr, bool count = true);
+  int32_t keep_block();  // bank_keep: the block a bank-served file read goes to, or -1 (a staging buffer)
   int32_t take_stage();
   void publish(Mover::Stream s, uint32_t k, int32_t v);
   bool fetch(uint32_t g, uint32_t unit, bool prefetch);
@@ -479,7 +556,8 @@ class SlotCache {
   void clear_dirty();
   void upload();
   LifoPool free_slots_, free_blocks_;
-  KeyList recent_, homes_;  // homes_: the file tier's pinned homes, front = most recently homed
+  KeyList recent_;
+  HomeList homes_;  // the file tier's pinned homes, front = most recently homed
   uint32_t on_device_ = 0, backed_ = 0, on_file_ = 0;
   OpenState open_;
   uint32_t stage_next_ = 0;

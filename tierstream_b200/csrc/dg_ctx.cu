@@ -146,6 +146,7 @@ void check_dg_options(const ss_budget& b, const ss_options& o, const PeerTier* p
        "dg_disk_prefetch / dg_disk_staging / dg_disk_queue need dg_disk_tier = 1"},
       {o.dg_disk_staging <= 256, "dg_disk_staging must be 0..256"},
       {o.dg_disk_queue <= 64 || o.dg_disk_queue == kQueueAuto, "dg_disk_queue must be 0..64 or SS_DG_DISK_QUEUE_AUTO"},
+      {o.dg_bank_keep <= 2, "dg_bank_keep must be 0, 1 or 2"},
   };
   for (const Need& n : invalid)
     if (!n.ok) dg_refuse(SS_E_INVALID, n.why);
@@ -158,7 +159,7 @@ void check_dg_options(const ss_budget& b, const ss_options& o, const PeerTier* p
   for (const auto& f : flags)
     if (f.first > 1) dg_refuse(SS_E_INVALID, std::string(f.second) + " must be 0 or 1");
   if (o.dg_disk_tier && peer) dg_refuse(SS_E_UNSUPPORTED, "the file tier with the peer tier is not in this build");
-  if (o.dg_landing_blocks || o.dg_bank_keep || o.dg_disk_queue_adapt || o.dg_prior_len)
+  if (o.dg_landing_blocks || o.dg_disk_queue_adapt || o.dg_prior_len)
     dg_refuse(SS_E_UNSUPPORTED, "an opt-in device-gated policy of the reference that is not in this build is set");
 }
 
@@ -1580,6 +1581,7 @@ class CudaDgContext final : public DgContext {
     s.pf_reverted = d(c.pf_reverted, base_.pf_reverted);
     s.pf_revert_bytes = d(c.pf_revert_bytes, base_.pf_revert_bytes);
     s.pf_strict_refused = d(c.pf_strict_refused, base_.pf_strict_refused);
+    s.bank_kept = d(c.bank_kept, base_.bank_kept);
     s.disk_queue_resolved = x_.disk_queue;
     s.disk_locations = x_.disk_tier && o_.dg_disk_queue == 0xFFFFFFFFu ? 1u : 0u;
     std::memcpy(out, &s, sizeof s);
@@ -1641,7 +1643,8 @@ class CudaDgContext final : public DgContext {
                   "\"prefetched\":%llu,\"bank_serves\":%llu,\"evicted\":%llu,\"resurrected\":%llu,"
                   "\"writebacks_done\":%llu,\"wb_issued_bytes\":%llu,\"free_slots\":%llu,\"land_launches\":%llu,"
                   "\"dma_ms_total\":%.6f,\"open_seconds\":%.3f,\"disk_reads\":%llu,\"disk_read_bytes\":%llu,"
-                  "\"disk_read_ns\":%llu,\"disk_drops\":%llu,\"disk_discards\":%llu,\"disk_units\":%llu},"
+                  "\"disk_read_ns\":%llu,\"disk_drops\":%llu,\"disk_discards\":%llu,\"disk_units\":%llu,"
+                  "\"bank_keep\":%u,\"bank_kept\":%llu,\"bank_keep_drops\":%llu,\"bank_keep_rereads\":%llu},"
                   "\"peer\":{\"world\":%u,\"rank\":%d,"
                   "\"all_owned\":%d,\"copy\":\"%s\",\"layout\":\"%s\",\"peer_units\":%llu,\"self_units\":%llu,"
                   "\"peer_bytes\":%llu,\"self_bytes\":%llu},"
@@ -1661,7 +1664,10 @@ class CudaDgContext final : public DgContext {
                   mover_->dma_total_ms(), open_seconds_, (unsigned long long)s.disk_reads,
                   (unsigned long long)s.disk_read_bytes, (unsigned long long)s.disk_read_ns,
                   (unsigned long long)s.disk_drops, (unsigned long long)s.disk_discards,
-                  (unsigned long long)s.disk_units, peer_ ? peer_->world : 0u, peer_ ? peer_->rank : -1,
+                  (unsigned long long)s.disk_units, o_.dg_bank_keep, (unsigned long long)s.bank_kept,
+                  (unsigned long long)(core_->stats().bank_keep_drops - base_.bank_keep_drops),
+                  (unsigned long long)(core_->stats().bank_keep_rereads - base_.bank_keep_rereads),
+                  peer_ ? peer_->world : 0u, peer_ ? peer_->rank : -1,
                   peer_ && peer_->all_owned ? 1 : 0, peer_ && peer_->copy == 1 ? "copy-engine" : "land-kernel",
                   peer_ && peer_->layout == kStriped ? "striped" : "whole-units",
                   (unsigned long long)mover_->peer_units(), (unsigned long long)mover_->self_units(),
@@ -2071,6 +2077,7 @@ class CudaDgContext final : public DgContext {
     c.clean_evict = o_.dg_clean_evict != 0;  // (no effect without the file tier)
     c.pf_revert = o_.dg_pf_revert_unused != 0;
     c.pf_strict = o_.dg_pf_strict_admit != 0;
+    c.bank_keep = o_.dg_bank_keep;  // (0..2; no effect without the file tier or with dg_no_admit)
     if (x_.disk_tier) {  // a file miss: the unit's parts from their files, checked against the descriptor's hash
       unsigned n = 8;
       if (const char* e = std::getenv("TSB_FILE_READERS")) n = unsigned(std::max(1L, std::min(64L, std::atol(e))));

@@ -120,6 +120,7 @@ void dg_replay(const tsb_dg_replay_config* c, const int32_t* ids, const int32_t*
   cfg.clean_evict = c->clean_evict != 0;
   cfg.pf_revert = c->pf_revert != 0;
   cfg.pf_strict = c->pf_strict != 0;
+  cfg.bank_keep = c->bank_keep;
   uint32_t keys = 0;
   for (uint32_t g = 0; g < c->n_gated; ++g) keys += c->n_units[g];
   HostMover m(std::vector<uint64_t>(c->part_bytes, c->part_bytes + c->n_parts), keys,
@@ -240,6 +241,14 @@ void dg_replay(const tsb_dg_replay_config* c, const int32_t* ids, const int32_t*
       const CacheStats& q = core.stats();
       const uint64_t pv[5] = {q.clean_drops, q.clean_drop_bytes, q.pf_reverted, q.pf_revert_bytes, q.pf_strict_refused};
       std::memcpy(c->pstats + size_t(t) * 5, pv, sizeof pv);
+    }
+    if (c->kstats) {  // the pinned homes' order as FNV-1a 64 over each key's 4 little-endian bytes
+      const CacheStats& q = core.stats();
+      uint64_t h = 0xcbf29ce484222325ull;
+      for (uint32_t k : core.host_order())
+        for (int b = 0; b < 4; ++b) h = (h ^ ((k >> (8 * b)) & 0xffu)) * 0x100000001b3ull;
+      const uint64_t kv[4] = {q.bank_kept, q.bank_keep_drops, q.bank_keep_rereads, h};
+      std::memcpy(c->kstats + size_t(t) * 4, kv, sizeof kv);
     }
     std::memcpy(tables + size_t(t) * keys, m.table_.data(), size_t(keys) * 4);
     const CacheStats& s = core.stats();

@@ -19,7 +19,7 @@ class DgSetup:
     def __init__(self, model, residents_per_layer=None, resident_keys=None, spare_per_layer=1, max_ids=2,
                  host_spare_units=None, diag=False, test_hooks=True, wb_defer=1, wb_stream=1, verify=False,
                  timeout_ms=10000, device_bytes=None, resident_order=None, inclusive=0, disk_keys=(), disk_staging=0,
-                 disk_prefetch=0, disk_queue=0, policy=0, weights=None, profile=None):
+                 disk_prefetch=0, disk_queue=0, policy=0, weights=None, profile=None, bank_keep=0):
         G, U = model.layers, model.units
         tiers = [abi.SS_TIER_PINNED] * (G * U)
         if resident_keys is None:
@@ -72,6 +72,7 @@ class DgSetup:
             o.dg_disk_staging = disk_staging
             o.dg_disk_prefetch = disk_prefetch
             o.dg_disk_queue = disk_queue
+            o.dg_bank_keep = bank_keep  # bank-served file reads kept in pinned blocks (1: recency front, 2: middle)
         self.budget, self.options = b, o
 
 
