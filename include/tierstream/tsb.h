@@ -229,6 +229,17 @@ SS_API ss_status tsb_test_sha256(const void* data, uint64_t len, uint8_t* out);
 SS_API ss_status tsb_test_score_profile(const ss_desc* d, const void* profile, uint64_t len, uint8_t* identity,
                                         uint32_t* cells, uint64_t cells_cap);
 
+/* Test hook of the adaptive read depth (dg_disk_queue_adapt): a depth controller of bound `bound` fed n busy periods
+ * (reads[i], bytes[i], ns[i]); depth[i] = the depth it returns after period i. params (may be NULL: the defaults
+ * 32, 512, 4096, 8192, 0.03, 0.25): min_reads, recheck_u, backoff_1, backoff_max, bar, drift. counters[11] at the end:
+ * changes, calibrations, windows, reads at 1, bytes at 1, busy ns at 1, reads at U, bytes at U, busy ns at U,
+ * verdicts, calibrating (0 / 1). verdicts[16][7] (may be NULL), the last ones, oldest first: number, reads before it,
+ * depth from, depth to, mean rate at U, mean rate at 1 (bytes / ns), reason (0 start, 1 keep U, 2 keep 1, 3 split,
+ * 4 recheck, 5 drift); *n_verdicts = how many are filled. */
+SS_API ss_status tsb_test_read_depth(uint32_t bound, const double* params, uint32_t n, const uint64_t* reads,
+                                     const uint64_t* bytes, const uint64_t* ns, uint32_t* depth, uint64_t* counters,
+                                     double* verdicts, uint32_t* n_verdicts);
+
 /* ---- Host xxh64 (this library's, the one the open's fill checks pinned units with; seed 0 in the descriptor) ---- */
 SS_API uint64_t tsb_xxh64(const void* data, size_t len, uint64_t seed);
 

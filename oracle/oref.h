@@ -78,6 +78,10 @@ typedef struct oref_dg_config {
  * and src_units (keys x unit_bytes, each unit's bytes) are given, read_sum receives per (token, g, id) the checksum
  * sum(byte * (pos % 251 + 1)) of the bytes found through the slot table after the layer's demand (0 for an absent
  * entry). Returns 0, or -1 with the message in err. */
+/* The reference's adaptive read depth controller fed n busy periods (reads, bytes, ns); the outputs of the library's
+ * tsb_test_read_depth. params (may be NULL): min_reads, recheck_u, backoff_1, backoff_max, bar, drift. */
+int oref_read_depth(uint32_t bound, const double* params, uint32_t n, const uint64_t* reads, const uint64_t* bytes,
+                    const uint64_t* ns, uint32_t* depth, uint64_t* counters, double* verdicts, uint32_t* n_verdicts);
 int oref_dg_replay(const oref_dg_config* cfg, const int32_t* ids, const int32_t* preds, int32_t* tables,
                    uint64_t* stats, const uint8_t* src_units, uint64_t* read_sum, char* err, size_t errlen);
 

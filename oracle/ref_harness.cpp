@@ -310,3 +310,36 @@ extern "C" __attribute__((visibility("default"))) int oref_dg_replay(const oref_
 }
 
 extern "C" __attribute__((visibility("default"))) unsigned oref_copy_threads(void) { return copy_threads(); }
+
+// The reference's adaptive read depth controller (src/dg_load.hpp:151-206) fed busy periods: the same outputs as
+// tsb_test_read_depth (depth after each period, 11 counters, the verdict ring as 7 doubles each).
+#include "dg_load.hpp"
+extern "C" __attribute__((visibility("default"))) int oref_read_depth(uint32_t bound, const double* params, uint32_t n,
+                                                                       const uint64_t* reads, const uint64_t* bytes,
+                                                                       const uint64_t* ns, uint32_t* depth,
+                                                                       uint64_t* counters, double* verdicts,
+                                                                       uint32_t* n_verdicts) {
+  ts::DgDepthCtl::Params p;
+  if (params) {
+    p.min_reads = uint64_t(params[0]);
+    p.recheck_u = uint64_t(params[1]);
+    p.backoff_1 = uint64_t(params[2]);
+    p.backoff_max = uint64_t(params[3]);
+    p.bar = params[4];
+    p.drift = params[5];
+  }
+  ts::DgDepthCtl c(bound, p);
+  for (uint32_t i = 0; i < n; ++i) depth[i] = c.on_busy(reads[i], bytes[i], ns[i]);
+  const uint64_t v[11] = {c.changes, c.calibrations, c.windows, c.reads1, c.bytes1, c.ns1,
+                          c.readsu, c.bytesu, c.nsu, c.decisions(), c.calibrating() ? 1u : 0u};
+  std::memcpy(counters, v, sizeof v);
+  uint32_t at = 0;
+  for (const ts::DgDepthCtl::Decision& d : c.ring()) {
+    const double row[7] = {double(d.seq), double(d.reads), double(d.from), double(d.to), d.rate_u, d.rate_1,
+                           double(d.reason)};
+    std::memcpy(verdicts + size_t(at) * 7, row, sizeof row);
+    ++at;
+  }
+  *n_verdicts = at;
+  return 0;
+}

@@ -1,7 +1,7 @@
 """The device-gated layout ss_open takes (slots, banks, blocks, spare and file units, staging buffers, the resolved
 read depth and score weights, the residents) against the reference's own dg_layout on the same descriptor, tiers,
 budget and options, on the CPU: every number is identical, or both refuse with the same status. Options this build
-refuses as unsupported (landings, adaptive depth, priors) are left out; host read-ahead, which both refuse with
+refuses as unsupported (landings, priors) are left out; host read-ahead, which both refuse with
 SS_E_INVALID in this mode, is tests/test_open_refusals.py's."""
 import ctypes as C
 import os
@@ -89,6 +89,8 @@ def random_case(seed, tmp):
             setattr(o, f, 1)
     if r.random() < 0.2:
         o.dg_bank_keep = int(r.integers(1, 3))
+    if r.random() < 0.15:  # (refused by both without the file tier or with a queue other than AUTO)
+        o.dg_disk_queue_adapt = 1
     return desc_json, tiers, b, o
 
 

@@ -448,6 +448,54 @@ def test_file_tier_bank_keep_matches_reference(small_model, orc, ref, monkeypatc
         run.close()
 
 
+def test_file_tier_adaptive_read_depth(small_model, orc, ref, monkeypatch):
+    """dg_disk_queue_adapt with reads in flight (dg_disk_queue AUTO, resolved to 3 with 3 staging buffers): the pool
+    runs its demand reads at the depth its controller measures faster, 1 or 3; what is read does not change, so every
+    routed unit's bytes and the slot table after every token equal the reference replay at a queue of 3, and the stats
+    report the controller (on, calibrations begun, its depth, the reads it measured at each depth)."""
+    import json
+    monkeypatch.setenv("TSB_DG_DETERMINISTIC", "1")
+    m = small_model
+    ids = synth.zipf_trace(60, m.layers, m.units, 2, s=0.6, seed=27)
+    run, res, disk = file_tier_run(m, S=3, verify=True, disk_queue=0xFFFFFFFF, disk_queue_adapt=1)
+    try:
+        cfg = file_tier_cfg(run, m, res, disk, ids, 3, disk_queue=3)
+        x_ref = np.zeros((ids.shape[0], 6), dtype=np.uint64)
+        t_ref, s_ref = oracle.ref_replay(cfg, ids, xstats=x_ref)
+        want = expected_sums(m, orc)
+        for t in range(ids.shape[0]):
+            got = run.step(ids[t])
+            keys = np.arange(m.layers)[:, None] * m.units + ids[t]
+            assert np.array_equal(got, want[keys]), "token %d read wrong bytes" % t
+            assert np.array_equal(run.ctx.table(run.keys), t_ref[t]), "slot table differs after token %d" % t
+        st = run.ctx.stats()
+        assert st["disk_reads"] == x_ref[-1][0] > 64 and st["misses"] == s_ref[-1][2]
+        j = json.loads(run.ctx.stats_json())
+        assert j["disk_queue_adapt"] == "on"
+        dd = j["disk_depth"]
+        assert dd["bound"] == 3 and dd["depth"] in (1, 3) and dd["calibrations"] >= 1 and dd["windows"] >= 1
+        assert 0 < dd["reads_1"] + dd["reads_u"] <= st["disk_reads"]
+        assert all(v["to"] in (1, 3) for v in dd["ring"])
+        run.ctx.check()
+        run.ctx.reset_open()  # a fresh calibration
+        j = json.loads(run.ctx.stats_json())
+        assert j["disk_depth"]["calibrations"] == 1 and j["disk_depth"]["windows"] == 0
+    finally:
+        run.close()
+
+
+def test_file_tier_adaptive_read_depth_declined(small_model, monkeypatch):
+    """dg_disk_queue_adapt is declined (the pool runs as without it, the stats say why) with a single reader and with
+    file prefetches."""
+    import json
+    for kw, why in ((dict(S=1), "one reader"), (dict(S=3, n_pred=2, disk_prefetch=1), "file prefetches")):
+        run, _, _ = file_tier_run(small_model, disk_queue=0xFFFFFFFF, disk_queue_adapt=1, **kw)
+        try:
+            assert json.loads(run.ctx.stats_json())["disk_queue_adapt"] == "declined: " + why
+        finally:
+            run.close()
+
+
 def test_file_tier_predictions_read_files(small_model, orc, ref, monkeypatch):
     """dg_disk_prefetch: predictions read file units too (on the prefetch stream, covered by the demand's wait)."""
     monkeypatch.setenv("TSB_DG_DETERMINISTIC", "1")

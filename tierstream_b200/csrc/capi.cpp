@@ -14,6 +14,7 @@
 #include "json.hpp"
 #include "peer.hpp"
 #include "plan.hpp"
+#include "read_depth.hpp"
 #include "resident_set.hpp"
 #include "score_profile.hpp"
 #include "strix_stream/ss.h"
@@ -746,6 +747,40 @@ ss_status tsb_test_sha256(const void* data, uint64_t len, uint8_t* out) {
     need((data || !len) && out, "tsb_test_sha256: null argument");
     const std::string h = tsb::sha256(data, size_t(len));
     std::memcpy(out, h.data(), 32);
+  });
+}
+
+ss_status tsb_test_read_depth(uint32_t bound, const double* params, uint32_t n, const uint64_t* reads,
+                              const uint64_t* bytes, const uint64_t* ns, uint32_t* depth, uint64_t* counters,
+                              double* verdicts, uint32_t* n_verdicts) {
+  return guard([&] {
+    need((reads && bytes && ns && depth) || !n, "tsb_test_read_depth: null argument");
+    tsb::ReadDepth::Params p;
+    if (params) {
+      p.min_reads = uint64_t(params[0]);
+      p.recheck_u = uint64_t(params[1]);
+      p.backoff_1 = uint64_t(params[2]);
+      p.backoff_max = uint64_t(params[3]);
+      p.bar = params[4];
+      p.drift = params[5];
+    }
+    tsb::ReadDepth c(bound, p);
+    for (uint32_t i = 0; i < n; ++i) depth[i] = c.on_busy(reads[i], bytes[i], ns[i]);
+    if (counters) {
+      const uint64_t v[11] = {c.changes, c.calibrations, c.windows, c.reads_1, c.bytes_1, c.ns_1,
+                              c.reads_u, c.bytes_u, c.ns_u, c.verdicts(), c.calibrating() ? 1u : 0u};
+      std::memcpy(counters, v, sizeof v);
+    }
+    uint32_t at = 0;
+    for (const tsb::ReadDepth::Verdict& v : c.recent()) {
+      if (verdicts) {
+        const double row[7] = {double(v.seq), double(v.reads), double(v.from), double(v.to), v.rate_u, v.rate_1,
+                               double(v.why)};
+        std::memcpy(verdicts + size_t(at) * 7, row, sizeof row);
+      }
+      ++at;
+    }
+    if (n_verdicts) *n_verdicts = at;
   });
 }
 

@@ -147,6 +147,9 @@ void check_dg_options(const ss_budget& b, const ss_options& o, const PeerTier* p
       {o.dg_disk_staging <= 256, "dg_disk_staging must be 0..256"},
       {o.dg_disk_queue <= 64 || o.dg_disk_queue == kQueueAuto, "dg_disk_queue must be 0..64 or SS_DG_DISK_QUEUE_AUTO"},
       {o.dg_bank_keep <= 2, "dg_bank_keep must be 0, 1 or 2"},
+      {o.dg_disk_queue_adapt <= 1, "dg_disk_queue_adapt must be 0 or 1"},
+      {!o.dg_disk_queue_adapt || (o.dg_disk_tier && o.dg_disk_queue == kQueueAuto),
+       "dg_disk_queue_adapt needs dg_disk_tier = 1 and dg_disk_queue = SS_DG_DISK_QUEUE_AUTO"},
   };
   for (const Need& n : invalid)
     if (!n.ok) dg_refuse(SS_E_INVALID, n.why);
@@ -159,7 +162,7 @@ void check_dg_options(const ss_budget& b, const ss_options& o, const PeerTier* p
   for (const auto& f : flags)
     if (f.first > 1) dg_refuse(SS_E_INVALID, std::string(f.second) + " must be 0 or 1");
   if (o.dg_disk_tier && peer) dg_refuse(SS_E_UNSUPPORTED, "the file tier with the peer tier is not in this build");
-  if (o.dg_landing_blocks || o.dg_disk_queue_adapt || o.dg_prior_len)
+  if (o.dg_landing_blocks || o.dg_prior_len)
     dg_refuse(SS_E_UNSUPPORTED, "an opt-in device-gated policy of the reference that is not in this build is set");
 }
 
@@ -1583,6 +1586,14 @@ class CudaDgContext final : public DgContext {
     s.pf_strict_refused = d(c.pf_strict_refused, base_.pf_strict_refused);
     s.bank_kept = d(c.bank_kept, base_.bank_kept);
     s.disk_queue_resolved = x_.disk_queue;
+    s.disk_depth_adapt = adapt_;  // (properties of the open's controller since open / reset_open)
+    s.disk_depth_active = x_.disk_tier ? x_.disk_queue : 0;
+    if (adapt_ == 1)
+      async_->with_depth([&](const ReadDepth& c) {
+        s.disk_depth_active = c.depth();
+        s.disk_depth_changes = c.changes;
+        s.disk_depth_calibrations = c.calibrations;
+      });
     s.disk_locations = x_.disk_tier && o_.dg_disk_queue == 0xFFFFFFFFu ? 1u : 0u;
     std::memcpy(out, &s, sizeof s);
   }
@@ -1636,8 +1647,8 @@ class CudaDgContext final : public DgContext {
   std::string stats_json() const override {
     ss_dg_stats s;
     stats(&s);
-    char buf[4096];
-    std::snprintf(buf, sizeof buf,
+    char buf[8192];
+    const int len = std::snprintf(buf, sizeof buf,
                   "{\"schema\":\"strix-stream/stats-v1\",\"mode\":\"device-gated\",\"copy\":\"%s\","
                   "\"dg\":{\"tokens\":%llu,\"lookups\":%llu,\"misses\":%llu,\"covered\":%llu,\"fetched\":%llu,"
                   "\"prefetched\":%llu,\"bank_serves\":%llu,\"evicted\":%llu,\"resurrected\":%llu,"
@@ -1682,7 +1693,46 @@ class CudaDgContext final : public DgContext {
                   (unsigned long long)mover_->check_stats().merged,
                   (unsigned long long)mover_->check_stats().hold_waits, (unsigned long long)check_failed_,
                   (unsigned long long)check_repaired_, check_wait_s_);
-    return buf;
+    require(len > 0 && size_t(len) < sizeof buf, SS_E_BACKEND, "device-gated: the stats text does not fit its buffer");
+    std::string out(buf);
+    out.pop_back();  // the closing brace: the read depth's section follows
+    out += adapt_json();
+    out += '}';
+    return out;
+  }
+  // ,"disk_queue_adapt":"on"|"off"|"declined: <why>" and, adapting, the controller's state and its verdict ring
+  std::string adapt_json() const {
+    std::string out = std::string(",\"disk_queue_adapt\":\"") +
+                      (adapt_ == 1 ? "on" : adapt_ == 2 ? std::string("declined: ") + adapt_why_ : "off") + "\"";
+    if (adapt_ != 1) return out;
+    async_->with_depth([&](const ReadDepth& c) {
+      char b[640];
+      std::snprintf(b, sizeof b,
+                    ",\"disk_depth\":{\"depth\":%u,\"bound\":%u,\"calibrating\":%d,\"changes\":%llu,"
+                    "\"calibrations\":%llu,\"windows\":%llu,\"decisions\":%llu,\"reads_1\":%llu,\"bytes_1\":%llu,"
+                    "\"busy_ns_1\":%llu,\"reads_u\":%llu,\"bytes_u\":%llu,\"busy_ns_u\":%llu,\"ring\":[",
+                    c.depth(), c.bound(), c.calibrating() ? 1 : 0, (unsigned long long)c.changes,
+                    (unsigned long long)c.calibrations, (unsigned long long)c.windows, (unsigned long long)c.verdicts(),
+                    (unsigned long long)c.reads_1, (unsigned long long)c.bytes_1, (unsigned long long)c.ns_1,
+                    (unsigned long long)c.reads_u, (unsigned long long)c.bytes_u, (unsigned long long)c.ns_u);
+      out += b;
+      static const char* const kWhy[] = {"start", "keep_u", "keep_1", "split", "recheck", "drift"};
+      const char* sep = "";
+      for (const ReadDepth::Verdict& v : c.recent()) {  // (rates in bytes / ns = GB/s)
+        std::snprintf(b, sizeof b,
+                      "%s{\"seq\":%llu,\"reads\":%llu,\"from\":%u,\"to\":%u,\"gbps_u\":%.6g,\"gbps_1\":%.6g,"
+                      "\"reason\":\"%s\"}",
+                      sep, (unsigned long long)v.seq, (unsigned long long)v.reads, v.from, v.to, v.rate_u, v.rate_1,
+                      kWhy[v.why]);
+        out += b;
+        sep = ",";
+      }
+      out += "]}";
+    });
+    return out;
+  }
+  void arm_adapt() {
+    if (adapt_ == 1) async_->set_depth(std::make_unique<ReadDepth>(x_.disk_queue), x_.unit_bytes);
   }
   void reset_open() override {
     require(!in_token_, SS_E_INVALID, "ss_dg_reset_open: between tokens only");
@@ -1691,6 +1741,7 @@ class CudaDgContext final : public DgContext {
       for (auto& k : keep_) k.clear();
       std::fill(held_.begin(), held_.end(), uint8_t(0));
       held_changed();
+      arm_adapt();  // (a fresh calibration: every read has ended)
     } catch (...) {
       poisoned_ = true;
       throw;
@@ -2097,6 +2148,15 @@ class CudaDgContext final : public DgContext {
         });
         mover_->set_async(async_.get());
       }
+      // dg_disk_queue_adapt: the pool's demand reads at a measured depth (1 or the resolved queue); declined where
+      // the pool is not demand-only over several readers
+      if (o_.dg_disk_queue_adapt) {
+        adapt_ = 2;
+        if (!async_) adapt_why_ = "one reader";
+        else if (o_.dg_disk_prefetch) adapt_why_ = "file prefetches";
+        else adapt_ = 1;
+      }
+      arm_adapt();
     }
     core_ = std::make_unique<SlotCache>(c, mover_.get());
     std::vector<uint32_t> order;
@@ -2401,6 +2461,8 @@ class CudaDgContext final : public DgContext {
   std::unique_ptr<ReadPool> readers_;                        // file tier: the reads of one miss at once
   std::vector<std::unique_ptr<ReadPool>> flight_pools_;      // file tier: one per reader thread of async_
   std::unique_ptr<AsyncReads> async_;                        // file tier: reads in flight (dg_disk_queue > 1)
+  uint32_t adapt_ = 0;            // dg_disk_queue_adapt: 0 off, 1 adapting (async_'s controller), 2 declined
+  const char* adapt_why_ = "";    // (declined: why)
   CudaMover::Buffers bufs_;
   uint32_t* ctl_ = nullptr;
   uint64_t* expect_dev_ = nullptr;  // the landing check: descriptor hashes in key order

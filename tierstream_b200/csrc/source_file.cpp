@@ -109,8 +109,20 @@ void SourceFile::read(void* dst, uint64_t offset, uint64_t bytes) const {
 }
 
 AsyncReads::AsyncReads(unsigned threads, std::function<void(uint32_t, char*, unsigned)> read)
-    : read_(std::move(read)) {
+    : read_(std::move(read)), limit_(std::max(1u, threads)) {
   for (unsigned i = 0; i < std::max(1u, threads); ++i) th_.emplace_back([this, i] { loop(i); });
+}
+
+void AsyncReads::set_depth(std::unique_ptr<ReadDepth> c, uint64_t unit_bytes) {
+  {
+    std::lock_guard<std::mutex> lk(mu_);
+    depth_ = std::move(c);
+    unit_bytes_ = unit_bytes;
+    const unsigned readers = unsigned(th_.size());
+    limit_ = depth_ ? std::min(std::max(depth_->depth(), 1u), readers) : readers;
+    busy_ = false;
+  }
+  cv_.notify_all();
 }
 
 AsyncReads::~AsyncReads() {
@@ -157,7 +169,8 @@ void AsyncReads::loop(unsigned worker) {
     Job* j = nullptr;
     {
       std::unique_lock<std::mutex> lk(mu_);
-      cv_.wait(lk, [&] { return stop_ || head_ < q_.size(); });
+      // (stopping drains the queue without the depth limit)
+      cv_.wait(lk, [&] { return (stop_ || reading_ < limit_) && (head_ < q_.size() || stop_); });
       if (head_ == q_.size()) return;  // (stopping with nothing queued)
       j = q_[head_++];
       if (head_ == q_.size()) {  // the queue's storage reused once every job was taken
@@ -165,6 +178,12 @@ void AsyncReads::loop(unsigned worker) {
         head_ = 0;
       }
       running_.push_back(j);
+      ++reading_;
+      if (depth_ && !busy_) {  // the pool leaves idle: a busy period begins
+        busy_ = true;
+        busy_t0_ = std::chrono::steady_clock::now();
+        busy_reads_ = 0;
+      }
     }
     const auto t0 = std::chrono::steady_clock::now();
     try {
@@ -174,11 +193,25 @@ void AsyncReads::loop(unsigned worker) {
     }
     j->ns = uint64_t(
         std::chrono::duration_cast<std::chrono::nanoseconds>(std::chrono::steady_clock::now() - t0).count());
+    bool more = false;
     {
       std::lock_guard<std::mutex> lk(mu_);
       j->done.store(true, std::memory_order_release);
+      --reading_;
+      if (depth_ && busy_) {
+        ++busy_reads_;
+        if (reading_ == 0 && head_ == q_.size()) {  // idle again: the period measured, the next depth set
+          const uint64_t ns = uint64_t(std::chrono::duration_cast<std::chrono::nanoseconds>(
+                                           std::chrono::steady_clock::now() - busy_t0_).count());
+          busy_ = false;
+          const uint32_t d = depth_->on_busy(busy_reads_, busy_reads_ * unit_bytes_, ns);
+          limit_ = std::min(std::max(d, 1u), unsigned(th_.size()));
+        }
+      }
+      more = head_ < q_.size();
     }
     done_cv_.notify_all();
+    if (more) cv_.notify_one();  // (a read held back by the depth may start)
   }
 }
 

@@ -4,6 +4,7 @@
 #pragma once
 
 #include <atomic>
+#include <chrono>
 #include <condition_variable>
 #include <cstdint>
 #include <exception>
@@ -12,6 +13,8 @@
 #include <string>
 #include <thread>
 #include <vector>
+
+#include "read_depth.hpp"
 
 namespace tsb {
 
@@ -31,6 +34,15 @@ class AsyncReads {
   void* begin(uint32_t key, char* dst);
   bool done(void* h) const;
   uint64_t end(void* h);
+  // dg_disk_queue_adapt: reads start only while fewer than the controller's depth run (the readers stay allocated),
+  // and each busy period of the pool (from idle to idle) is measured and fed to it, each read counted as
+  // unit_bytes. Set while idle (the open, reset_open); nullptr: every reader.
+  void set_depth(std::unique_ptr<ReadDepth> c, uint64_t unit_bytes);
+  template <class F>
+  void with_depth(F&& f) const {  // f(const ReadDepth&) under the pool's lock, if a controller is set
+    std::lock_guard<std::mutex> lk(mu_);
+    if (depth_) f(*depth_);
+  }
 
  private:
   struct Job {
@@ -42,13 +54,20 @@ class AsyncReads {
   };
   void loop(unsigned worker);
   std::function<void(uint32_t, char*, unsigned)> read_;
-  std::mutex mu_;
+  mutable std::mutex mu_;
   std::condition_variable cv_, done_cv_;
   std::vector<Job*> q_;                    // queued, oldest first (owned)
   std::vector<Job*> running_;              // taken by a reader, not yet ended (owned)
   size_t head_ = 0;                        // the next queued job
   std::vector<std::thread> th_;
   bool stop_ = false;
+  unsigned reading_ = 0;                   // reads taken and not finished
+  unsigned limit_ = 0;                     // reads allowed at once (the readers, or the controller's depth)
+  std::unique_ptr<ReadDepth> depth_;       // dg_disk_queue_adapt's controller (or none)
+  uint64_t unit_bytes_ = 0;
+  bool busy_ = false;                      // a busy period is being measured
+  std::chrono::steady_clock::time_point busy_t0_;
+  uint64_t busy_reads_ = 0;
 };
 
 class ReadPool {

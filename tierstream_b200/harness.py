@@ -19,7 +19,8 @@ class DgSetup:
     def __init__(self, model, residents_per_layer=None, resident_keys=None, spare_per_layer=1, max_ids=2,
                  host_spare_units=None, diag=False, test_hooks=True, wb_defer=1, wb_stream=1, verify=False,
                  timeout_ms=10000, device_bytes=None, resident_order=None, inclusive=0, disk_keys=(), disk_staging=0,
-                 disk_prefetch=0, disk_queue=0, policy=0, weights=None, profile=None, bank_keep=0):
+                 disk_prefetch=0, disk_queue=0, policy=0, weights=None, profile=None, bank_keep=0,
+                 disk_queue_adapt=0):
         G, U = model.layers, model.units
         tiers = [abi.SS_TIER_PINNED] * (G * U)
         if resident_keys is None:
@@ -73,6 +74,7 @@ class DgSetup:
             o.dg_disk_prefetch = disk_prefetch
             o.dg_disk_queue = disk_queue
             o.dg_bank_keep = bank_keep  # bank-served file reads kept in pinned blocks (1: recency front, 2: middle)
+            o.dg_disk_queue_adapt = disk_queue_adapt  # (with disk_queue SS_DG_DISK_QUEUE_AUTO)
         self.budget, self.options = b, o
 
 
