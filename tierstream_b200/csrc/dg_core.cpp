@@ -1989,6 +1989,7 @@ void SlotCache::check() const {
     if (++homes_listed > keys_) broken("the pinned recency list has a cycle");
     if (e_[k].home != Home::Host) broken("a unit in the pinned recency list is not a pinned home");
   }
+  if (!homes_.consistent()) broken("the pinned recency list's front-half cursor");
   for (uint32_t k = 0; k < keys_; ++k) {
     const Entry& x = e_[k];
     const bool in_recent = recent_.has(k);

@@ -378,6 +378,17 @@ class SlotCache {
       --size_;
       settle();
     }
+    // The cursor's invariant, walked: the first size / 2 units are marked as the front half, none after them, and the
+    // cursor is the last marked one (none when the half is empty).
+    bool consistent() const {
+      uint32_t at = 0, last_front = kNil;
+      for (uint32_t k = list_.front(); k != kNil; k = list_.older(k), ++at) {
+        if (at > size_) return false;  // (a cycle)
+        if (bool(in_front_[k]) != (at < size_ / 2)) return false;
+        if (in_front_[k]) last_front = k;
+      }
+      return at == size_ && front_n_ == size_ / 2 && last_front == edge_;
+    }
 
    private:
     void grew() {
