@@ -804,16 +804,22 @@ def main():
         s2 = run.ctx.stats()
         outs2 = np.zeros((a.steps, LAYERS, TOP_K), dtype=np.uint64)
         step_ms = []
-        barrier()
-        w0 = time.perf_counter()
-        for t in range(a.steps):
-            ws = time.perf_counter()
-            outs2[t] = run.step(ids2[t], mode=0)
-            if a.round_every and (t + 1) % a.round_every == 0:
-                run.ctx.round()
-            step_ms.append((time.perf_counter() - ws) * 1e3)
-        w1 = time.perf_counter()
-        barrier()
+        import gc
+        gc.collect()  # the interpreter's collector off while the host drives the timed tokens (on again after)
+        gc.disable()
+        try:
+            barrier()
+            w0 = time.perf_counter()
+            for t in range(a.steps):
+                ws = time.perf_counter()
+                outs2[t] = run.step(ids2[t], mode=0)
+                if a.round_every and (t + 1) % a.round_every == 0:
+                    run.ctx.round()
+                step_ms.append((time.perf_counter() - ws) * 1e3)
+            w1 = time.perf_counter()
+            barrier()
+        finally:
+            gc.enable()
         # every routed unit of both legs as its reader saw it, against the generator's sums
         n1, bad1, first1 = harness.check_reads(outs_dev.cpu().numpy().view(np.uint64).reshape(a.steps, LAYERS, TOP_K),
                                                ids[a.warmup:], UNITS, want[1])
