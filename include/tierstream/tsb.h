@@ -124,6 +124,11 @@ typedef struct tsb_dg_replay_config {
   /* kstats (optional): [tokens][4] bank_kept, bank_keep_drops, bank_keep_rereads, and the FNV-1a 64 hash of the
    * pinned homes' recency order (gated keys as 4 little-endian bytes each, most recently homed first) */
   uint64_t* kstats;
+  /* landings: dg_landing_blocks and dg_landing_ttl (the reads are synchronous here); lstats (optional): [tokens][9]
+   * landing_issued, landing_promoted, landing_late, landing_expired, landing_dropped_full, landing_read_bytes,
+   * landing_expired_layer, landing_skipped_passed, and the units landed or landing after the boundary */
+  uint32_t landing_blocks, landing_ttl;
+  uint64_t* lstats;
 } tsb_dg_replay_config;
 SS_API ss_status tsb_test_dg_replay(const tsb_dg_replay_config* cfg, const int32_t* ids, const int32_t* preds,
                                     int32_t* tables, uint64_t* stats, const uint8_t* src_units, uint64_t* read_sum);

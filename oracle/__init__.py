@@ -104,7 +104,7 @@ def ref_host_replay(desc_json, tiers, budget, options, routes, all_layers, want_
 
 
 def ref_replay(cfg, ids, preds=None, src_units=None, want_reads=False, xstats=None, rstats=None, pstats=None,
-               qstats=None, mstats=None, sstats=None, kstats=None):
+               qstats=None, mstats=None, sstats=None, kstats=None, lstats=None):
     """The reference DgCore's deterministic replay on the same config struct: (tables, stats[, read_sum]). xstats: an
     optional uint64 array [tokens][6] for the three-tier counters (disk_reads, disk_read_bytes, disk_stage_waits,
     disk_drops, disk_discards, file units) after each boundary."""
@@ -117,6 +117,7 @@ def ref_replay(cfg, ids, preds=None, src_units=None, want_reads=False, xstats=No
     cfg.mstats = mstats.ctypes.data_as(C.POINTER(C.c_uint64)) if mstats is not None else None
     cfg.sstats = sstats.ctypes.data_as(C.POINTER(C.c_uint64)) if sstats is not None else None
     cfg.kstats = kstats.ctypes.data_as(C.POINTER(C.c_uint64)) if kstats is not None else None
+    cfg.lstats = lstats.ctypes.data_as(C.POINTER(C.c_uint64)) if lstats is not None else None
     ids = np.ascontiguousarray(ids, dtype=np.int32)
     tables = np.empty((cfg.tokens, keys), dtype=np.int32)
     stats = np.empty((cfg.tokens, 16), dtype=np.uint64)

@@ -65,6 +65,11 @@ typedef struct oref_dg_config {
   /* kstats (optional): [tokens][4] bank_kept, bank_keep_drops, bank_keep_rereads, FNV-1a 64 of the pinned homes'
    * recency order (keys as 4 little-endian bytes, most recently homed first) */
   uint64_t* kstats;
+  /* landings (dg_landing_blocks, dg_landing_ttl; synchronous reads); lstats (optional): [tokens][9] landing_issued,
+   * landing_promoted, landing_late, landing_expired, landing_dropped_full, landing_read_bytes, landing_expired_layer,
+   * landing_skipped_passed, units landed or landing */
+  uint32_t landing_blocks, landing_ttl;
+  uint64_t* lstats;
 } oref_dg_config;
 #define OREF_NXSTATS 6
 

@@ -48,7 +48,7 @@ class HostTransport final : public ts::DgTransport {
     // buffers each, far above a host's last-level cache for the benchmark's units (the bytes read back through the
     // table are then not meaningful)
     alias_slots_ = c.move_bytes == 2 ? 16 : slots;
-    alias_blocks_ = c.move_bytes == 2 ? 16 : c.blocks + c.disk_staging;
+    alias_blocks_ = c.move_bytes == 2 ? 16 : c.blocks + c.disk_staging + c.landing_blocks;
     if (move_) {
       arena_.assign(size_t(alias_slots_) * unit_, 1);
       blocks_.assign(size_t(alias_blocks_) * unit_, 2);
@@ -151,6 +151,8 @@ extern "C" __attribute__((visibility("default"))) int oref_dg_replay(const oref_
     cfg.pf_revert = c->pf_revert != 0;
     cfg.pf_strict = c->pf_strict != 0;
     cfg.bank_keep = c->bank_keep;
+    cfg.landing_blocks = c->landing_blocks;
+    cfg.landing_ttl = c->landing_ttl;
     if (c->w_trans || c->w_freq || c->w_rec) {
       cfg.w_trans = c->w_trans;
       cfg.w_freq = c->w_freq;
@@ -287,6 +289,13 @@ extern "C" __attribute__((visibility("default"))) int oref_dg_replay(const oref_
           for (int b = 0; b < 4; ++b) h = (h ^ ((k >> (8 * b)) & 0xffu)) * 0x100000001b3ull;
         const uint64_t kv[4] = {q.bank_kept, q.bank_keep_drops, q.bank_keep_rereads, h};
         std::memcpy(c->kstats + size_t(tok) * 4, kv, sizeof kv);
+      }
+      if (c->lstats) {
+        const ts::DgStats& q = core.stats();
+        const uint64_t lv[9] = {q.landing_issued,  q.landing_promoted,     q.landing_late,
+                                q.landing_expired, q.landing_dropped_full, q.landing_read_bytes,
+                                q.landing_expired_layer, q.landing_skipped_passed, core.landing_units()};
+        std::memcpy(c->lstats + size_t(tok) * 9, lv, sizeof lv);
       }
       std::memcpy(tables + size_t(tok) * keys, t.table_.data(), size_t(keys) * 4);
       const ts::DgStats& s = core.stats();

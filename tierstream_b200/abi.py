@@ -149,7 +149,8 @@ class dg_replay_config(C.Structure):
                 ("pf_strict", u32), ("pstats", C.POINTER(u64)), ("disk_queue", u32), ("reserved3", u32),
                 ("qstats", C.POINTER(u64)), ("mr_n", u32), ("reserved4", u32), ("mr_token", C.POINTER(u32)),
                 ("mr_layer", C.POINTER(u32)), ("mr_count", C.POINTER(u32)), ("mr_ids", C.POINTER(u32)),
-                ("mstats", C.POINTER(u64)), ("sstats", C.POINTER(u64)), ("kstats", C.POINTER(u64))]
+                ("mstats", C.POINTER(u64)), ("sstats", C.POINTER(u64)), ("kstats", C.POINTER(u64)),
+                ("landing_blocks", u32), ("landing_ttl", u32), ("lstats", C.POINTER(u64))]
 
 
 class ss_dg_round_params(C.Structure):

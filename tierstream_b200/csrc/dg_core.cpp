@@ -42,7 +42,14 @@ SlotCache::SlotCache(const CacheConfig& cfg, Mover* m) : c_(cfg), m_(m) {
   require(!c_.no_admit || c_.bank_slots >= c_.max_ids, SS_E_CAPACITY,
           "device-gated: dg_no_admit serves every miss through a bank slot: it needs " + std::to_string(c_.max_ids) +
               " bank slots per bank (dg_max_ids), " + std::to_string(c_.bank_slots) + " configured");
+  require(!c_.landing_blocks || c_.disk_tier, SS_E_INVALID, "device-gated: landing blocks without the file tier");
+  require(uint64_t(c_.blocks) + c_.disk_staging + c_.landing_blocks < 0x7fffffffull, SS_E_INVALID,
+          "device-gated: too many landing blocks");
   stage_ev_.assign(c_.disk_staging, nullptr);
+  free_lands_.fill_down(int32_t(c_.landing_blocks), 0);  // (landing block 0 taken first)
+  land_owner_.assign(c_.landing_blocks, kNil);
+  served_.assign(c_.n_units.size(), 0);
+  late_.reserve(c_.max_ids);
   run_.assign(c_.n_units.size(), 1);
   dirty_lo_.assign(c_.n_units.size(), kNil);
   dirty_hi_.assign(c_.n_units.size(), 0);
@@ -88,6 +95,14 @@ SlotCache::~SlotCache() {
   for (const Pending& p : pending_) {  // a read in flight ends before the buffer it writes can be freed
     try {
       m_->read_end(p.handle);
+    } catch (...) {
+    }
+  }
+  for (const LandRead& r : landing_) {  // (a landing read: dropped if it has not started, else waited for)
+    Mover::LandingEnd end;
+    if (m_->read_landing_cancel(r.handle, &end)) continue;
+    try {
+      m_->read_landing_end(r.handle, &end);
     } catch (...) {
     }
   }
@@ -300,7 +315,11 @@ void SlotCache::place(const std::vector<uint32_t>& order, const std::vector<uint
   on_device_ = uint32_t(dev.size());
   free_slots_.fill_down(int32_t(c_.persistent_slots), int32_t(on_device_));
   free_blocks_.fill_down(int32_t(c_.blocks), blocks_used);
-  open_ = OpenState{c_, e_, table_, free_slots_, free_blocks_, recent_, homes_, on_device_, on_file_, stamp_};
+  free_lands_.fill_down(int32_t(c_.landing_blocks), 0);
+  land_owner_.assign(c_.landing_blocks, kNil);
+  on_land_ = 0;
+  open_ = OpenState{c_, e_, table_, free_slots_, free_blocks_, recent_, homes_, free_lands_, on_device_, on_file_,
+                    stamp_};
 }
 
 // ---- file tier ----
@@ -349,6 +368,153 @@ int32_t SlotCache::keep_block() {
     ++st_.bank_keep_drops;
   }
   return free_blocks_.take();
+}
+
+// ---- landings (landing_blocks): the file tier's two-stage prefetch ----
+// A landing holds exactly its key (Landing while its read runs, Landed after; its home is still its file: no slot,
+// block or entry) and one landing block. A failed landing read only frees its block (advice: a demand reads the unit
+// as any file miss).
+bool SlotCache::advise_land(uint32_t g, uint32_t unit) {
+  if (!c_.landing_blocks) return false;
+  const uint32_t k = key(g, unit);
+  const Home h = e_[k].home;
+  if (h == Home::Landing || h == Home::Landed) return true;
+  if (h != Home::File) return false;
+  if (c_.landing_ttl == 0 && served_[g]) {  // its layer's demand already passed this token: it could not be used
+    ++st_.landing_skipped_passed;
+    return true;
+  }
+  land(k);
+  return true;
+}
+
+bool SlotCache::land(uint32_t k) {
+  reclaim_lands(false);
+  if (free_lands_.empty()) {  // never displaces another landing
+    ++st_.landing_dropped_full;
+    return false;
+  }
+  const int32_t l = free_lands_.items().back();
+  void* handle = nullptr;
+  try {
+    handle = m_->read_landing_begin(k, land_block(l));
+  } catch (...) {  // nothing begun: the block stays free, the key in its file
+    ++st_.landing_failed;
+    return false;
+  }
+  free_lands_.take();
+  landing_.push_back(LandRead{k, l, handle, false});
+  land_owner_[size_t(l)] = k;
+  Entry& x = e_[k];
+  x.home = Home::Landing;
+  x.land = l;
+  x.land_age = 0;
+  --on_file_;
+  ++on_land_;
+  ++st_.landing_issued;
+  return true;
+}
+
+bool SlotCache::end_landing(size_t i) {
+  const LandRead r = landing_[i];
+  landing_.erase(landing_.begin() + std::ptrdiff_t(i));
+  Mover::LandingEnd end;
+  bool ok = true;
+  try {
+    m_->read_landing_end(r.handle, &end);
+  } catch (...) {  // advice: its error is dropped (a demand's own read reports one)
+    ok = false;
+  }
+  st_.landing_yields += end.yields;
+  if (!ok) {
+    ++st_.landing_failed;
+    unland(r.key);
+    return false;
+  }
+  st_.landing_read_bytes += unit_bytes_ - end.aborted_bytes;
+  st_.landing_aborted_bytes += end.aborted_bytes;
+  if (r.doomed || end.aborted) {  // its layer passed undemanded: never promoted, its block free
+    unland(r.key);
+    ++st_.landing_expired_layer;
+    return false;
+  }
+  e_[r.key].home = Home::Landed;
+  return true;
+}
+
+void SlotCache::end_landings() {
+  while (!landing_.empty()) end_landing(0);
+}
+
+void SlotCache::poll_landings(size_t max) {
+  for (size_t i = 0, seen = 0; i < landing_.size() && seen < max; ++seen) {
+    if (m_->read_done(landing_[i].handle)) end_landing(i);
+    else ++i;
+  }
+}
+
+bool SlotCache::cancel_landing(size_t i) {
+  Mover::LandingEnd end;
+  if (!m_->read_landing_cancel(landing_[i].handle, &end)) return false;
+  const uint32_t k = landing_[i].key;
+  landing_.erase(landing_.begin() + std::ptrdiff_t(i));
+  unland(k);
+  ++st_.landing_cancelled;
+  st_.landing_yields += end.yields;
+  st_.landing_aborted_bytes += end.aborted_bytes;
+  if (end.aborted_bytes) st_.landing_read_bytes += unit_bytes_ - end.aborted_bytes;  // (yielded part-way)
+  return true;
+}
+
+void SlotCache::cancel_landings() {
+  for (size_t i = 0; i < landing_.size();)
+    if (!cancel_landing(i)) ++i;
+}
+
+// landing_ttl 0, layer g's demand served: a landing of layer g that it did not route cannot be used this token. A
+// landed one goes back to its file now; one not running is cancelled; a running one is asked to stop and goes back
+// to its file when it ends.
+void SlotCache::expire_layer_landings(uint32_t g, const uint32_t* ids, uint32_t n) {
+  const uint32_t first = base_[g], last = base_[g + 1];
+  for (uint32_t l = 0; l < c_.landing_blocks; ++l) {
+    const uint32_t k = land_owner_[l];
+    if (k == kNil || k < first || k >= last || std::find(ids, ids + n, k - first) != ids + n) continue;
+    if (e_[k].home == Home::Landed) {
+      unland(k);
+      ++st_.landing_expired_layer;
+      continue;
+    }
+    size_t i = 0;
+    while (landing_[i].key != k) ++i;
+    if (!cancel_landing(i)) {
+      landing_[i].doomed = true;
+      m_->read_landing_abort(landing_[i].handle);
+    }
+  }
+}
+
+void SlotCache::unland(uint32_t k) {
+  Entry& x = e_[k];
+  free_lands_.give(x.land);
+  land_owner_[size_t(x.land)] = kNil;
+  x.land = -1;
+  x.land_age = 0;
+  x.home = Home::File;
+  --on_land_;
+  ++on_file_;
+}
+
+void SlotCache::reclaim_lands(bool synced) {
+  size_t kept = 0;
+  for (const LandBusy& b : land_busy_) {
+    if (synced || m_->done(b.ev)) {
+      free_lands_.give(b.land);
+      pool_.push_back(b.ev);
+    } else {
+      land_busy_[kept++] = b;
+    }
+  }
+  land_busy_.resize(kept);
 }
 
 // The next staging buffer in rotation, once a read still holding it ended and its last copy landed.
@@ -637,6 +803,7 @@ void SlotCache::begin_token(uint32_t seq, const std::vector<uint8_t>* run) {
   pf_token_ = demand_free_used_ = 0;
   std::fill(pf_layer_.begin(), pf_layer_.end(), 0u);
   std::fill(layer_missed_.begin(), layer_missed_.end(), uint8_t(0));
+  std::fill(served_.begin(), served_.end(), uint8_t(0));
   pred_.clear();
   pred_layer_ = kNil;
 }
@@ -673,6 +840,20 @@ bool SlotCache::resurrect(uint32_t k) {
 bool SlotCache::fetch(uint32_t g, uint32_t unit, bool prefetch) {
   const uint32_t k = key(g, unit);
   Entry& x = e_[k];
+  if (x.home == Home::Landing || x.home == Home::Landed) {
+    if (prefetch) return false;  // a landing is promoted by a demand only
+    if (x.home == Home::Landing) {  // its read ends now, out of order (failed: a file miss below, as any)
+      size_t i = 0;
+      while (landing_[i].key != k) ++i;
+      const bool late = !m_->read_done(landing_[i].handle);
+      const auto t0 = Clock::now();
+      const bool ok = end_landing(i);
+      if (late) {
+        st_.landing_wait_ns += ns_since(t0);
+        st_.landing_late += ok ? 1 : 0;
+      }
+    }
+  }
   if (prefetch && (c_.no_admit || pf_layer_[g] >= c_.prefetch_per_layer || pf_token_ >= c_.prefetch_per_token))
     return false;
   if (x.home == Home::Coming) {
@@ -753,6 +934,18 @@ bool SlotCache::fetch(uint32_t g, uint32_t unit, bool prefetch) {
       st_.bank_keep_rereads += st_.tokens + 1 - x.keep_drop <= 8 ? 1 : 0;
       x.keep_drop = 0;
     }
+  } else if (x.home == Home::Landed) {  // from its landing block, free again once this copy's event completed
+    if (mut_ == kEntryBeforeCopy) publish(s, k, slot);
+    m_->h2d(s, slot, land_block(x.land), k);
+    if (mut_ != kEntryBeforeCopy) publish(s, k, slot);
+    void* ev = event();
+    m_->record(ev, s);
+    land_busy_.push_back(LandBusy{x.land, ev});
+    land_owner_[size_t(x.land)] = kNil;
+    x.land = -1;
+    x.land_age = 0;
+    --on_land_;
+    ++st_.landing_promoted;
   } else {
     if (mut_ == kEntryBeforeCopy) publish(s, k, slot);  // test-only fault: the entry before its bytes
     m_->h2d(s, slot, x.block, k);
@@ -825,16 +1018,29 @@ void SlotCache::serve_demand(uint32_t g, const uint32_t* ids, uint32_t n, uint64
             "device-gated: layer " + std::to_string(g) + " exported id " + std::to_string(ids[i]) + " of " +
                 std::to_string(nu));
   if (mask) m_->diag_mark(g, 0);
-  // masked occurrences in export order: a repeated id is fetched at its first occurrence, covered at the others
+  // masked occurrences in export order: a repeated id is fetched at its first occurrence, covered at the others; a
+  // miss whose landing read still runs is fetched after the layer's other misses (their reads start first)
+  late_.clear();
+  uint64_t late_covered = 0;
+  poll_landings();  // (a landing read that completed is landed: only a running one is late)
   for (uint32_t i = 0; i < n; ++i) {
     if (!((mask >> i) & 1u)) continue;
     const Home h = e_[key(g, ids[i])].home;
-    if (h != Home::Device && h != Home::Coming && h != Home::Bank) {
+    if (h == Home::Device || h == Home::Coming || h == Home::Bank) {
+      cover(g, ids[i]);
+      ++st_.covered;
+    } else if (c_.landing_blocks && h == Home::Landing) {
+      if (std::find(late_.begin(), late_.end(), ids[i]) != late_.end()) ++late_covered;
+      else late_.push_back(ids[i]);
+    } else {
       fetch(g, ids[i], false);
-      continue;
     }
-    cover(g, ids[i]);
-    ++st_.covered;
+  }
+  for (uint32_t id : late_) fetch(g, id, false);
+  st_.covered += late_covered;  // (a repeated late miss: covered at its later occurrences)
+  if (c_.landing_blocks && c_.landing_ttl == 0) {
+    served_[g] = 1;
+    expire_layer_landings(g, ids, n);
   }
   drain_layer(g, ids, n);  // this layer's copies and entries (its demand reads, the prefetch reads it routes)
   if (!mask) return;
@@ -879,7 +1085,8 @@ void SlotCache::serve_prediction(uint32_t g_next, const uint32_t* pred, uint32_t
   st_.predicted += uniq_.size();
   pred_ = uniq_;
   pred_layer_ = g_next;
-  for (uint32_t id : pred_) fetch(g_next, id, true);
+  for (uint32_t id : pred_)
+    if (!advise_land(g_next, id)) fetch(g_next, id, true);  // (landings on: a file-homed unit lands instead)
 }
 
 // ---- the boundary ----
@@ -887,6 +1094,20 @@ void SlotCache::end_token(const std::vector<uint32_t>& keep, uint32_t rows) {
   drain_pending();  // the end of the token: no read in flight while its streams sync and victims are chosen
   m_->sync(Mover::kDem);
   m_->sync(Mover::kPf);
+  if (c_.landing_blocks) {
+    // the landing reads not running are dropped, the running ones end (landed, or back to their file); every landing
+    // block a promotion's copy read is free (the streams synced); a landing not demanded for landing_ttl boundaries
+    // (TTL 0: one) goes back to its file, with no copy
+    cancel_landings();
+    end_landings();
+    reclaim_lands(true);
+    for (uint32_t l = 0; l < c_.landing_blocks; ++l) {
+      const uint32_t k = land_owner_[l];
+      if (k == kNil || ++e_[k].land_age < std::max<uint32_t>(c_.landing_ttl, 1)) continue;
+      unland(k);
+      ++st_.landing_expired;
+    }
+  }
   std::vector<uint8_t> held;
   if (!keep.empty()) {
     held.assign(keys_, 0);
@@ -923,6 +1144,7 @@ void SlotCache::end_token(const std::vector<uint32_t>& keep, uint32_t rows) {
     }
   }
   coming_.clear();
+  std::fill(served_.begin(), served_.end(), uint8_t(0));
   // (2) bank units go back to their blocks (or, read from it, their file)
   for (uint32_t k : banked_) {
     Entry& x = e_[k];
@@ -1263,6 +1485,7 @@ SlotCache::ResidentResult SlotCache::make_resident(uint32_t g, const std::vector
 
   std::vector<uint8_t> hold = want;  // never dropped to a file here: the units to copy in, this call's write-backs
   std::vector<int32_t> released;     // source blocks of committed copies (free once the demand stream synced)
+  std::vector<int32_t> released_lands;  // the same of landed units' landing blocks
   std::vector<int32_t> written;      // slots of written-back victims (free once the write-back stream synced)
   struct Read {
     uint32_t key;
@@ -1310,6 +1533,8 @@ SlotCache::ResidentResult SlotCache::make_resident(uint32_t g, const std::vector
     m_->sync(Mover::kDem);
     for (int32_t b : released) free_blocks_.give(b);
     released.clear();
+    for (int32_t l : released_lands) free_lands_.give(l);
+    released_lands.clear();
   };
   auto settle_writes = [&] {
     if (written.empty()) return;
@@ -1406,6 +1631,18 @@ SlotCache::ResidentResult SlotCache::make_resident(uint32_t g, const std::vector
         commit(k, slot);
         continue;
       }
+      if (x.home == Home::Landed) {  // its landing block is the source, as a pinned block (drained: landed)
+        const int32_t l = x.land;
+        copy_in(k, slot, land_block(l));
+        ++next;
+        released_lands.push_back(l);
+        land_owner_[size_t(l)] = kNil;
+        x.land = -1;
+        x.land_age = 0;
+        --on_land_;
+        commit(k, slot);
+        continue;
+      }
       // its file, through the next staging buffer (its last copy landed first): at most `depth` reads in flight, the
       // finished ones ending first (any position), then the oldest; a read holding the next buffer ends before it
       try {
@@ -1464,8 +1701,10 @@ SlotCache::ResidentResult SlotCache::make_resident(uint32_t g, const std::vector
     if (!uploaded) {  // a device failure: the host records stay one ownership (the context is poisoned by its caller)
       for (int32_t s : written) free_slots_.give(s);
       for (int32_t b : released) free_blocks_.give(b);
+      for (int32_t l : released_lands) free_lands_.give(l);
       written.clear();
       released.clear();
+      released_lands.clear();
     }
     account();
     throw;
@@ -1766,8 +2005,11 @@ uint32_t SlotCache::seed(const std::vector<uint32_t>& keys) {
 
 void SlotCache::drain() {
   drain_pending();
+  cancel_landings();  // (the ones not running: back to their files; the others landed, or back on a failure)
+  end_landings();
   while (!deferred_.empty()) finish_front();
   for (Mover::Stream s : {Mover::kDem, Mover::kPf, Mover::kD2h}) m_->sync(s);
+  reclaim_lands(true);
 }
 
 std::vector<uint32_t> SlotCache::residency() const {
@@ -1835,6 +2077,8 @@ void SlotCache::reset_open() {
     }
   for (void* ev : stage_ev_)  // every staging copy landed
     if (ev) m_->event_sync(ev);
+  for (uint32_t l = 0; l < c_.landing_blocks; ++l)  // landings (ended: none reads its block) back to their files
+    if (land_owner_[l] != kNil) unland(land_owner_[l]);
   const size_t P = c_.persistent_slots, N = P + c_.blocks, kStage = N, kFile = N + 1;
   std::vector<size_t> at(keys_), goal(keys_);
   std::vector<uint32_t> holder(N + 1, kNil), wants(N + 1, kNil);  // per location: its unit now, the unit it should hold
@@ -1942,6 +2186,9 @@ void SlotCache::reset_open() {
   free_blocks_ = open_.blocks;
   recent_ = open_.recent;
   homes_ = open_.homes;
+  free_lands_ = open_.lands;  // (every landing block free, in the open's order)
+  on_land_ = 0;
+  std::fill(served_.begin(), served_.end(), uint8_t(0));
   on_device_ = open_.on_device;
   on_file_ = open_.on_file;
   stage_next_ = 0;
@@ -1969,7 +2216,7 @@ void SlotCache::reset_open() {
 
 // ---- invariants ----
 void SlotCache::check() const {
-  std::vector<uint8_t> slot_owner(slots_, 0), block_owner(c_.blocks, 0);
+  std::vector<uint8_t> slot_owner(slots_, 0), block_owner(c_.blocks, 0), land_owner(c_.landing_blocks, 0);
   auto own = [this](std::vector<uint8_t>& v, int64_t i, const char* what) {
     if (i < 0 || size_t(i) >= v.size() || v[size_t(i)]) broken(what);
     v[size_t(i)] = 1;
@@ -1980,7 +2227,7 @@ void SlotCache::check() const {
         const uint32_t g = gated_of(k);
         if (k < dirty_lo_[g] || k > dirty_hi_[g]) broken("a table entry changed without its mark");
       }
-  uint32_t listed = 0, homes_listed = 0, dev = 0, hosts = 0, files = 0;
+  uint32_t listed = 0, homes_listed = 0, dev = 0, hosts = 0, files = 0, lands = 0, landing_n = 0;
   for (uint32_t k = recent_.front(); k != kNil; k = recent_.older(k)) {
     if (++listed > keys_) broken("the recency list has a cycle");
     if (e_[k].home != Home::Device && e_[k].home != Home::Coming) broken("a listed unit is not on the device");
@@ -1993,6 +2240,7 @@ void SlotCache::check() const {
   for (uint32_t k = 0; k < keys_; ++k) {
     const Entry& x = e_[k];
     const bool in_recent = recent_.has(k);
+    if ((x.land >= 0) != (x.home == Home::Landing || x.home == Home::Landed)) broken("a landing block outside a landing");
     switch (x.home) {
       case Home::Host:
         own(block_owner, x.block, "a host unit without its own block");
@@ -2033,8 +2281,31 @@ void SlotCache::check() const {
         own(block_owner, x.block, "an evicting unit without its destination block");
         if (table_[k] != -1) broken("an evicting unit with a published entry");
         break;
+      case Home::Landing:
+      case Home::Landed:
+        if (!c_.disk_tier || !c_.landing_blocks) broken("a landing without landing blocks");
+        if (x.slot >= 0 || x.block >= 0 || table_[k] != -1 || in_recent || homes_.has(k) || x.pf_done)
+          broken("a landing holding a slot, a block, an entry or a copy event");
+        own(land_owner, x.land, "a landing without its own landing block");
+        if (land_owner_[size_t(x.land)] != k) broken("a landing block's owner is another unit");
+        if (x.home == Home::Landed && x.land_age >= std::max<uint32_t>(c_.landing_ttl, 1))
+          broken("a landing past its time to live");
+        ++lands;
+        landing_n += x.home == Home::Landing ? 1 : 0;
+        break;
     }
   }
+  for (const LandRead& r : landing_)
+    if (r.key >= keys_ || e_[r.key].home != Home::Landing || e_[r.key].land != r.land)
+      broken("a landing read does not match its unit");
+  if (landing_.size() != landing_n) broken("the landing reads disagree with the units landing");
+  for (const LandBusy& b : land_busy_) own(land_owner, b.land, "a landing block behind a copy and in use");
+  for (int32_t l : free_lands_.items()) own(land_owner, l, "a free landing block that is also in use");
+  for (uint32_t l = 0; l < c_.landing_blocks; ++l) {
+    if (!land_owner[l]) broken("a landing block neither free nor held");
+    if (land_owner_[l] != kNil && e_[land_owner_[l]].land != int32_t(l)) broken("a landing block's owner");
+  }
+  if (lands != on_land_) broken("the landing count disagrees with the homes");
   if (dev != on_device_ || dev != listed) broken("the device count disagrees with the homes");
   if (files != on_file_) broken("the file count disagrees with the homes");
   if (c_.disk_tier && hosts != homes_listed) broken("the pinned recency list does not hold every pinned home");

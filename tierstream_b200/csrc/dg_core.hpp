@@ -79,6 +79,28 @@ class Mover {
     (void)handle;
     return true;
   }
+  // Landings (landing_blocks): the same checked read into landing block `block` (blocks + disk_staging + l), behind
+  // every demand read not started yet, ended and queried like read_begin's handles (ending one still queued starts
+  // it first). A landing read not running can be cancelled (true: nothing more is written to its block and the handle
+  // is gone; false: it runs or ran, end it as usual) and a running one asked to stop early (it is still ended). How
+  // one ended: aborted (stopped before its end: its block holds part of the unit), the bytes it did not read, the
+  // times it gave its reader to a demand read. Defaults: the plain read, never cancelled or stopped.
+  struct LandingEnd {
+    uint64_t aborted_bytes = 0;
+    uint32_t yields = 0;
+    bool aborted = false;
+  };
+  virtual void* read_landing_begin(uint32_t key, int32_t block) { return read_begin(key, block); }
+  virtual uint64_t read_landing_end(void* handle, LandingEnd* end) {
+    *end = LandingEnd{};
+    return read_end(handle);
+  }
+  virtual bool read_landing_cancel(void* handle, LandingEnd* end) noexcept {
+    (void)handle;
+    *end = LandingEnd{};
+    return false;
+  }
+  virtual void read_landing_abort(void* handle) noexcept { (void)handle; }
   // slot_of[key] = v after everything enqueued on s so far (a release at system scope).
   virtual void publish(Stream s, uint32_t key, int32_t v) = 0;
   // ready[g] = seq on kDem after everything enqueued there.
@@ -140,6 +162,14 @@ struct CacheConfig {
   // list (1), or after its front half (2), so that a unit read once does not push out the most recently homed ones
   // (dg_core.cpp:237-250, 1286-1303, 142-160, 200-213).
   uint32_t bank_keep = 0;
+  // landing_blocks (file tier, reads in flight): a prediction of a file-homed unit reads it into one of this many
+  // pinned landing blocks instead of a slot (no slot taken, nothing evicted, outside the prefetch budgets; no free
+  // landing block: the advice is dropped); a demand then copies it from there (a read still running ends first, never
+  // a second read). landing_ttl 0: a landing its layer did not route goes back to its file right after that layer's
+  // demand, and a prediction for a layer already served this token is not issued; N >= 1: a landing not demanded
+  // for N boundaries goes back to its file. Every read in flight ends at the boundary (dg_core.cpp:440-612,
+  // 1146-1162, 1216-1222, 1309-1324, 1439-1460, 1633, 1648-1662, 2499-2511, 2910-2919, 2997-2999).
+  uint32_t landing_blocks = 0, landing_ttl = 0;
 };
 
 struct CacheStats {
@@ -170,6 +200,13 @@ struct CacheStats {
   // bank_keep: file reads kept in a pinned block; pinned units dropped to their file for one; of those, the ones read
   // back from their file within 8 tokens
   uint64_t bank_kept = 0, bank_keep_drops = 0, bank_keep_rereads = 0;
+  // landings: reads begun; demands served from a landing block (late ones included) and of those the ones whose read
+  // was still running, with the host's wait for them; landings back to their file unused (TTL); advice dropped with no
+  // free landing block; bytes landed; reads that failed; reads cancelled before running; (TTL 0) landings their layer
+  // did not route and predictions for a layer already served; a chunked read's yields and the bytes it did not read
+  uint64_t landing_issued = 0, landing_promoted = 0, landing_late = 0, landing_wait_ns = 0, landing_expired = 0;
+  uint64_t landing_dropped_full = 0, landing_read_bytes = 0, landing_failed = 0, landing_cancelled = 0;
+  uint64_t landing_expired_layer = 0, landing_skipped_passed = 0, landing_yields = 0, landing_aborted_bytes = 0;
   // make_resident: units copied in and evicted, bytes copied in, host time; its file reads, their bytes and time,
   // its write-back bytes
   uint64_t resident_units = 0, resident_evicted = 0, resident_bytes = 0, resident_ns = 0;
@@ -196,7 +233,8 @@ struct LayerCounts {
 
 class SlotCache {
  public:
-  enum class Home : uint8_t { Host, Device, Coming, Bank, Evicting, File };
+  // Landing / Landed (landing_blocks): a file home whose landing read is running / done, holding a landing block
+  enum class Home : uint8_t { Host, Device, Coming, Bank, Evicting, File, Landing, Landed };
   enum Mutation { kNone0 = 0, kEntryBeforeCopy = 1, kNoCover = 2 };
 
   SlotCache(const CacheConfig& cfg, Mover* m);
@@ -225,7 +263,8 @@ class SlotCache {
   uint32_t free_blocks() const { return uint32_t(free_blocks_.size()); }
   uint32_t deferred() const { return uint32_t(deferred_.size()); }
   uint32_t backed_units() const { return backed_; }
-  uint32_t file_units() const { return on_file_; }
+  uint32_t file_units() const { return on_file_ + on_land_; }  // (landings' homes are their files)
+  uint32_t landing_units() const { return on_land_; }
   // Pinned homes, most recently homed first (file tier only).
   std::vector<uint32_t> host_order() const;
   uint64_t wb_outstanding_bytes() const { return outstanding_; }
@@ -437,6 +476,8 @@ class SlotCache {
     bool wb_pending = false, via_pf = false, used = false;
     bool backed = false;  // a device unit whose block still holds its bytes (inclusive share)
     bool keep_mid = false;  // bank_keep 2: a kept read, homed behind the pinned list's front half when released
+    int32_t land = -1;      // Landing / Landed: its landing block
+    uint32_t land_age = 0;  // Landed: boundaries passed since
     uint64_t keep_drop = 0;  // bank_keep: tokens + 1 when dropped to its file for a kept read (0: not)
     uint64_t demand_epoch = 0, lru_stamp = 0;  // scored: the last token that routed it; its recency list position
     void* pf_done = nullptr;
@@ -462,6 +503,7 @@ class SlotCache {
     LifoPool slots, blocks;
     KeyList recent;
     HomeList homes;
+    LifoPool lands;
     uint32_t on_device = 0, on_file = 0;
     uint64_t stamp = 0;
   };
@@ -543,6 +585,29 @@ class SlotCache {
   // the least recently homed pinned unit not in `skip` to its file; count: a disk drop of the boundary
   bool drop_host_lru(const std::vector<uint8_t>* skip = nullptr, bool count = true);
   int32_t keep_block();  // bank_keep: the block a bank-served file read goes to, or -1 (a staging buffer)
+  // ---- landings ----
+  struct LandRead {
+    uint32_t key;
+    int32_t land;
+    void* handle;
+    bool doomed;  // (TTL 0) its layer passed while it ran: back to its file when it ends
+  };
+  struct LandBusy {  // a landing block a promotion's copy still reads, free once the event completed
+    int32_t land;
+    void* ev;
+  };
+  static bool file_homed(Home h) { return h == Home::File || h == Home::Landing || h == Home::Landed; }
+  int32_t land_block(int32_t l) const { return int32_t(c_.blocks + c_.disk_staging) + l; }
+  bool advise_land(uint32_t g, uint32_t unit);  // true: the landing path took the advice
+  bool land(uint32_t k);
+  bool end_landing(size_t i);                   // false: failed or doomed (the key back to its file)
+  void end_landings();                          // every read in flight, oldest first
+  void poll_landings(size_t max = SIZE_MAX);    // the completed ones among the max oldest
+  bool cancel_landing(size_t i);
+  void cancel_landings();                       // the ones not running
+  void expire_layer_landings(uint32_t g, const uint32_t* ids, uint32_t n);
+  void unland(uint32_t k);                      // back to its file, its landing block free
+  void reclaim_lands(bool synced);              // landing blocks whose promotion copy landed back to the free list
   int32_t take_stage();
   void publish(Mover::Stream s, uint32_t k, int32_t v);
   bool fetch(uint32_t g, uint32_t unit, bool prefetch);
@@ -574,6 +639,13 @@ class SlotCache {
   uint32_t stage_next_ = 0;
   std::vector<void*> stage_ev_;  // per staging buffer: its last copy's event
   std::vector<Pending> pending_;  // file reads in flight, oldest first
+  LifoPool free_lands_;
+  std::vector<uint32_t> land_owner_;  // per landing block: its Landing / Landed key (kNil: none)
+  std::vector<LandRead> landing_;     // landing reads in flight, oldest first
+  std::vector<LandBusy> land_busy_;
+  std::vector<uint8_t> served_;       // (TTL 0) the layers whose demand this token served
+  std::vector<uint32_t> late_;        // a layer's misses whose landing read still runs (fetched after the others)
+  uint32_t on_land_ = 0;
   uint64_t entries_ = 0;          // public calls so far (a read ended in a later one was carried)
   std::vector<LayerScore> sc_;
   std::vector<uint8_t> run_;

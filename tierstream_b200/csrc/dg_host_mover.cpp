@@ -121,10 +121,13 @@ void dg_replay(const tsb_dg_replay_config* c, const int32_t* ids, const int32_t*
   cfg.pf_revert = c->pf_revert != 0;
   cfg.pf_strict = c->pf_strict != 0;
   cfg.bank_keep = c->bank_keep;
+  cfg.landing_blocks = c->landing_blocks;
+  cfg.landing_ttl = c->landing_ttl;
   uint32_t keys = 0;
   for (uint32_t g = 0; g < c->n_gated; ++g) keys += c->n_units[g];
   HostMover m(std::vector<uint64_t>(c->part_bytes, c->part_bytes + c->n_parts), keys,
-              c->persistent_slots + 2 * c->bank_slots + 1, c->blocks + c->disk_staging, c->move_bytes != 0, src_units);
+              c->persistent_slots + 2 * c->bank_slots + 1, c->blocks + c->disk_staging + c->landing_blocks,
+              c->move_bytes != 0, src_units);
   SlotCache core(cfg, &m);
   std::vector<uint32_t> order(c->order, c->order + c->n_order);
   for (uint32_t k = 0; k < keys; ++k) order.push_back(k);
@@ -249,6 +252,13 @@ void dg_replay(const tsb_dg_replay_config* c, const int32_t* ids, const int32_t*
         for (int b = 0; b < 4; ++b) h = (h ^ ((k >> (8 * b)) & 0xffu)) * 0x100000001b3ull;
       const uint64_t kv[4] = {q.bank_kept, q.bank_keep_drops, q.bank_keep_rereads, h};
       std::memcpy(c->kstats + size_t(t) * 4, kv, sizeof kv);
+    }
+    if (c->lstats) {
+      const CacheStats& q = core.stats();
+      const uint64_t lv[9] = {q.landing_issued,  q.landing_promoted,    q.landing_late,
+                              q.landing_expired, q.landing_dropped_full, q.landing_read_bytes,
+                              q.landing_expired_layer, q.landing_skipped_passed, core.landing_units()};
+      std::memcpy(c->lstats + size_t(t) * 9, lv, sizeof lv);
     }
     std::memcpy(tables + size_t(t) * keys, m.table_.data(), size_t(keys) * 4);
     const CacheStats& s = core.stats();

@@ -281,7 +281,8 @@ def replay_config(n_units, part_bytes, persistent_slots, bank_slots, blocks, spa
                   wb_on_d2h=1, wb_layer_bytes=0, wb_max_outstanding=0, move_bytes=0, inclusive=0, disk=None,
                   home_blocks=0, disk_staging=0, disk_prefetch=0, policy=0, rows=1, weights=None, profile=None,
                   round_every=0, round_max_units=96, round_hysteresis=1.25, round_decay=0.85, round_budget=0,
-                  no_admit=0, clean_evict=0, pf_revert=0, pf_strict=0, disk_queue=0, resident_events=(), bank_keep=0):
+                  no_admit=0, clean_evict=0, pf_revert=0, pf_strict=0, disk_queue=0, resident_events=(), bank_keep=0,
+                  landing_blocks=0, landing_ttl=0):
     """A dg_replay_config with its arrays kept alive on the returned object. disk (file tier): one flag per key for
     the plan's disk units (blocks then counts home_blocks + the spare blocks); xstats is attached by replay().
     policy (scored eviction): 0 LRU, 1 SCORED, 2 SCORED_AUTO, with each boundary's row count `rows`, weights
@@ -306,6 +307,7 @@ def replay_config(n_units, part_bytes, persistent_slots, bank_slots, blocks, spa
     c.policy, c.rows = policy, rows
     c.no_admit, c.clean_evict, c.pf_revert, c.pf_strict = no_admit, clean_evict, pf_revert, pf_strict
     c.disk_queue, c.bank_keep = disk_queue, bank_keep
+    c.landing_blocks, c.landing_ttl = landing_blocks, landing_ttl
     if resident_events:  # (token, gated layer, ids): ss_dg_make_resident after that token's boundary; ids () = release
         ev = list(resident_events)
         keep["mr_token"] = (C.c_uint32 * len(ev))(*[e[0] for e in ev])
@@ -333,7 +335,7 @@ def replay_config(n_units, part_bytes, persistent_slots, bank_slots, blocks, spa
 
 
 def replay(cfg, ids, preds=None, src_units=None, want_reads=False, xstats=None, rstats=None, pstats=None,
-           qstats=None, mstats=None, sstats=None, kstats=None):
+           qstats=None, mstats=None, sstats=None, kstats=None, lstats=None):
     """This library's deterministic replay (tsb_test_dg_replay): (tables, stats[, read_sum]). xstats: an optional
     uint64 array [tokens][6] filled with the file tier's counters after each boundary."""
     keys = sum(cfg.n_units[i] for i in range(cfg.n_gated))
@@ -344,6 +346,7 @@ def replay(cfg, ids, preds=None, src_units=None, want_reads=False, xstats=None, 
     cfg.mstats = mstats.ctypes.data_as(C.POINTER(C.c_uint64)) if mstats is not None else None  # [tokens][4]
     cfg.sstats = sstats.ctypes.data_as(C.POINTER(C.c_uint64)) if sstats is not None else None  # [tokens][5]
     cfg.kstats = kstats.ctypes.data_as(C.POINTER(C.c_uint64)) if kstats is not None else None  # [tokens][4]
+    cfg.lstats = lstats.ctypes.data_as(C.POINTER(C.c_uint64)) if lstats is not None else None  # [tokens][9]
     ids = np.ascontiguousarray(ids, dtype=np.int32)
     tables = np.empty((cfg.tokens, keys), dtype=np.int32)
     stats = np.empty((cfg.tokens, 16), dtype=np.uint64)
