@@ -203,10 +203,11 @@ extern "C" __attribute__((visibility("default"))) int oref_dg_layout(const char*
     const ts::Desc d = ts::desc_from_json(ts::json_parse(std::string(desc_json, len)));
     const ts::Plan p = ts::plan_from_tiers(d, *budget, std::vector<uint8_t>(tiers, tiers + n_tiers));
     const ts::DgLayout x = ts::dg_layout(d, p, *opt);
-    const uint64_t v[23] = {x.keys, x.R, x.D, x.B, x.P, x.Q, x.I, x.F, x.S, x.disk_queue, x.blocks,
+    const uint64_t v[27] = {x.keys, x.R, x.D, x.B, x.P, x.Q, x.I, x.F, x.S, x.disk_queue, x.blocks,
                             x.persistent_slots, x.slots, x.guard_slot, x.unit_bytes, x.host_stride, x.disk_tier,
-                            x.disk_prefetch, x.scored, x.w_trans, x.w_freq, x.w_rec, x.residents.size()};
-    for (uint32_t i = 0; i < n_out && i < 23; ++i) out[i] = v[i];
+                            x.disk_prefetch, x.scored, x.w_trans, x.w_freq, x.w_rec, x.residents.size(),
+                            x.L, x.landing_queued, x.landing_ttl, x.landing_chunk};
+    for (uint32_t i = 0; i < n_out && i < 27; ++i) out[i] = v[i];
     for (uint32_t i = 0; i < cap && i < x.residents.size(); ++i) residents[i] = x.residents[i];
     return 0;
   } catch (const ts::Error& e) {

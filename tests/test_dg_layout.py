@@ -1,7 +1,7 @@
 """The device-gated layout ss_open takes (slots, banks, blocks, spare and file units, staging buffers, the resolved
 read depth and score weights, the residents) against the reference's own dg_layout on the same descriptor, tiers,
 budget and options, on the CPU: every number is identical, or both refuse with the same status. Options this build
-refuses as unsupported (landings, priors) are left out; host read-ahead, which both refuse with
+refuses as unsupported (window priors) are left out; host read-ahead, which both refuse with
 SS_E_INVALID in this mode, is tests/test_open_refusals.py's."""
 import ctypes as C
 import os
@@ -12,7 +12,7 @@ import pytest
 import oracle
 from tierstream_b200 import abi, runtime, synth
 
-N_OUT = 23
+N_OUT = 27
 
 
 def ours(desc_json, tiers, b, o):
@@ -91,6 +91,14 @@ def random_case(seed, tmp):
         o.dg_bank_keep = int(r.integers(1, 3))
     if r.random() < 0.15:  # (refused by both without the file tier or with a queue other than AUTO)
         o.dg_disk_queue_adapt = 1
+    if r.random() < 0.2:  # landing blocks (refused by both without the file tier or with a queue of 1)
+        o.dg_landing_blocks = int(r.choice([1, 4, 64, 4097]))
+        if r.random() < 0.5:
+            o.dg_landing_ttl = int(r.choice([0, 3, 1025]))
+        if r.random() < 0.3:
+            o.dg_landing_max_queued = int(r.choice([0, 2, 65]))
+        if r.random() < 0.3:
+            o.dg_landing_chunk = int(r.choice([0, 8192, 5000, 0xFFFFFFFF]))
     return desc_json, tiers, b, o
 
 
@@ -122,6 +130,32 @@ def test_bank_keep_values(ref, tmp_path):
         if st == abi.SS_OK:
             assert np.array_equal(out, r_out)
     assert b"dg_bank_keep" in abi.load().ss_last_error()
+
+
+def test_landing_values(ref, tmp_path):
+    """Landing blocks on a file-tier case with reads in flight: every count, TTL, queue and chunk setting gives the
+    reference's layout (the blocks charged to the host budget), or both refuse with the same status."""
+    for seed in range(150):
+        desc_json, tiers, b, o = random_case(seed, str(tmp_path))
+        if abi.SS_TIER_DISK not in tiers:
+            continue
+        o.dg_disk_tier, o.dg_disk_queue, o.dg_disk_queue_adapt = 1, 3, 0
+        o.dg_landing_blocks = o.dg_landing_ttl = o.dg_landing_max_queued = o.dg_landing_chunk = 0
+        if ours(desc_json, tiers, b, o)[0] == abi.SS_OK:
+            break
+    seen = set()
+    for blocks, ttl, queued, chunk, queue in ((1, 0, 0, 0, 3), (8, 2, 4, 8192, 3), (64, 1024, 64, 0xFFFFFFFF, 3),
+                                              (4, 0, 0, 0, 1), (0, 1, 0, 0, 3), (4096, 0, 0, 4096, 3),
+                                              (100000, 0, 0, 0, 3)):
+        o.dg_landing_blocks, o.dg_landing_ttl, o.dg_landing_max_queued, o.dg_landing_chunk = blocks, ttl, queued, chunk
+        o.dg_disk_queue = queue
+        st, out, _ = ours(desc_json, tiers, b, o)
+        r_st, r_out, _, r_err = reference(desc_json, tiers, b, o)
+        assert st == r_st, (blocks, ttl, queued, chunk, queue, st, r_st, r_err)
+        if st == abi.SS_OK:
+            assert np.array_equal(out, r_out), (blocks, out.tolist(), r_out.tolist())
+        seen.add(st)
+    assert abi.SS_OK in seen and abi.SS_E_INVALID in seen
 
 
 def test_layout_cases_are_mostly_accepted(ref, tmp_path):

@@ -496,6 +496,49 @@ def test_file_tier_adaptive_read_depth_declined(small_model, monkeypatch):
             run.close()
 
 
+@pytest.mark.parametrize("ttl", [0, 2])
+def test_file_tier_landing_blocks_match_reference(small_model, orc, ref, monkeypatch, ttl):
+    """dg_landing_blocks with reads in flight: predictions of file-homed units are read (and hashed) into landing
+    blocks on the read pool behind the demand reads; a demand copies them from there; unrouted landings expire at
+    their layer (TTL 0) or after 2 boundaries. Every routed unit's bytes are the source's, and the slot table, the file
+    counters and the landing counters after every token equal the reference DgCore's replay."""
+    import json
+    monkeypatch.setenv("TSB_DG_DETERMINISTIC", "1")
+    m = small_model
+    ids = synth.zipf_trace(40, m.layers, m.units, 2, s=0.8, seed=29)
+    preds = synth.zipf_trace(40, m.layers, m.units, 2, s=0.8, seed=30)
+    run, res, disk = file_tier_run(m, pinned=2, S=3, n_pred=2, disk_queue=0xFFFFFFFF, landing_blocks=4,
+                                   landing_ttl=ttl, verify=True)
+    try:
+        cfg = file_tier_cfg(run, m, res, disk, ids, 3, n_pred=2, disk_queue=3, landing_blocks=4, landing_ttl=ttl)
+        x_ref = np.zeros((ids.shape[0], 6), dtype=np.uint64)
+        l_ref = np.zeros((ids.shape[0], 9), dtype=np.uint64)
+        t_ref, s_ref = oracle.ref_replay(cfg, ids, preds, xstats=x_ref, lstats=l_ref)
+        want = expected_sums(m, orc)
+        for t in range(ids.shape[0]):
+            got = run.step(ids[t], preds[t])
+            keys = np.arange(m.layers)[:, None] * m.units + ids[t]
+            assert np.array_equal(got, want[keys]), "token %d read wrong bytes" % t
+            assert np.array_equal(run.ctx.table(run.keys), t_ref[t]), "slot table differs after token %d" % t
+        st = run.ctx.stats()
+        assert st["misses"] == s_ref[-1][2] and st["disk_reads"] == x_ref[-1][0]
+        lj = json.loads(run.ctx.stats_json())["landing"]
+        assert lj["blocks"] == 4 and lj["ttl"] == ttl
+        assert lj["issued"] == l_ref[-1][0] > 0 and lj["promoted"] == l_ref[-1][1] > 0
+        assert lj["expired"] == l_ref[-1][3] and lj["dropped_full"] == l_ref[-1][4]
+        assert lj["read_bytes"] == l_ref[-1][5] and lj["expired_layer"] == l_ref[-1][6]
+        assert lj["units"] == l_ref[-1][8] and lj["failed"] == 0
+        run.ctx.check()
+        for L in range(m.layers):
+            for u in range(m.units):
+                run.ctx.check_unit(L, u)
+        run.ctx.reset_open()  # landings back to their files, every landing block free
+        assert json.loads(run.ctx.stats_json())["landing"]["units"] == 0
+        run.ctx.check()
+    finally:
+        run.close()
+
+
 def test_file_tier_predictions_read_files(small_model, orc, ref, monkeypatch):
     """dg_disk_prefetch: predictions read file units too (on the prefetch stream, covered by the demand's wait)."""
     monkeypatch.setenv("TSB_DG_DETERMINISTIC", "1")

@@ -111,6 +111,9 @@ struct Layout {
   bool disk_tier = false, disk_prefetch = false;
   uint32_t F = 0, S = 0, disk_queue = 0;
   std::vector<uint8_t> disk;
+  // landing blocks (dg_landing_blocks, file tier only): L blocks after the staging buffers; the landing reads at once
+  // (dg_landing_max_queued, 0 = 1), the TTL and the chunk size (0 = whole reads)
+  uint32_t L = 0, landing_queued = 1, landing_ttl = 0, landing_chunk = 0;
   // scored eviction (SS_POLICY_SCORED / SCORED_AUTO): the weights and a profile's counts (empty: none)
   bool scored = false, scored_auto = false;
   uint32_t w_trans = 700, w_freq = 200, w_rec = 100;
@@ -147,6 +150,16 @@ void check_dg_options(const ss_budget& b, const ss_options& o, const PeerTier* p
       {o.dg_disk_staging <= 256, "dg_disk_staging must be 0..256"},
       {o.dg_disk_queue <= 64 || o.dg_disk_queue == kQueueAuto, "dg_disk_queue must be 0..64 or SS_DG_DISK_QUEUE_AUTO"},
       {o.dg_bank_keep <= 2, "dg_bank_keep must be 0, 1 or 2"},
+      {o.dg_landing_blocks <= 4096, "dg_landing_blocks must be 0..4096"},
+      {o.dg_landing_blocks || !(o.dg_landing_max_queued || o.dg_landing_ttl || o.dg_landing_chunk),
+       "dg_landing_max_queued / dg_landing_ttl / dg_landing_chunk need dg_landing_blocks > 0"},
+      {o.dg_landing_max_queued <= 64, "dg_landing_max_queued must be 0..64"},
+      {o.dg_landing_ttl <= 1024, "dg_landing_ttl must be 0..1024"},
+      {o.dg_landing_chunk == 0xFFFFFFFFu || o.dg_landing_chunk % 4096 == 0,
+       "dg_landing_chunk must be 0, a multiple of 4096 or 0xFFFFFFFF (no chunks)"},
+      {!o.dg_landing_blocks || o.dg_disk_tier, "dg_landing_blocks needs dg_disk_tier = 1"},
+      {!o.dg_landing_blocks || o.dg_disk_queue > 1,
+       "dg_landing_blocks needs dg_disk_queue > 1 (the landing reads run on the read pool)"},
       {o.dg_disk_queue_adapt <= 1, "dg_disk_queue_adapt must be 0 or 1"},
       {!o.dg_disk_queue_adapt || (o.dg_disk_tier && o.dg_disk_queue == kQueueAuto),
        "dg_disk_queue_adapt needs dg_disk_tier = 1 and dg_disk_queue = SS_DG_DISK_QUEUE_AUTO"},
@@ -162,7 +175,7 @@ void check_dg_options(const ss_budget& b, const ss_options& o, const PeerTier* p
   for (const auto& f : flags)
     if (f.first > 1) dg_refuse(SS_E_INVALID, std::string(f.second) + " must be 0 or 1");
   if (o.dg_disk_tier && peer) dg_refuse(SS_E_UNSUPPORTED, "the file tier with the peer tier is not in this build");
-  if (o.dg_landing_blocks || o.dg_prior_len)
+  if (o.dg_prior_len)
     dg_refuse(SS_E_UNSUPPORTED, "an opt-in device-gated policy of the reference that is not in this build is set");
 }
 
@@ -241,6 +254,11 @@ void place_homes(const Desc& d, const Plan& p, const ss_options& o, Layout& x) {
                                                   : std::max<uint32_t>(1, o.dg_disk_queue);
     x.S = staging ? staging : 8u;
   }
+  // landing blocks only with file units (nothing to land otherwise: dg_layout.cpp:343-347)
+  x.L = files ? o.dg_landing_blocks : 0u;
+  x.landing_queued = o.dg_landing_max_queued ? o.dg_landing_max_queued : 1u;
+  x.landing_ttl = o.dg_landing_ttl;
+  x.landing_chunk = o.dg_landing_chunk == 0xFFFFFFFFu ? 0u : o.dg_landing_chunk ? o.dg_landing_chunk : 4u << 20;
 }
 
 // Scored eviction (dg_layout.cpp:349-371): the three weights (per mille, summing to 1000, or all 0 for the
@@ -322,10 +340,10 @@ void size_arena(const Desc& d, const Plan& p, const ss_options& o, const PeerTie
   // host: the plan's pinned bytes, one reset unit and S staging units, and 1 MiB of mapped control words (none of
   // the blocks when every unit lives in a peer store)
   const bool no_blocks = peer && peer->all_owned;
-  const uint64_t pinned = p.pinned + (1ull + x.S) * x.host_stride + (uint64_t(1) << 20);
+  const uint64_t pinned = p.pinned + (1ull + x.S + x.L) * x.host_stride + (uint64_t(1) << 20);
   if (!no_blocks && pinned > b.host_pinned_bytes)
-    dg_refuse(SS_E_CAPACITY, "the plan's pinned bytes plus the staging units and the mapped control area exceed the "
-                             "host budget (" + std::to_string(b.host_pinned_bytes) + ")");
+    dg_refuse(SS_E_CAPACITY, "the plan's pinned bytes plus the staging units, the landing blocks and the mapped "
+                             "control area exceed the host budget (" + std::to_string(b.host_pinned_bytes) + ")");
 }
 
 Layout make_layout(const Desc& d, const Plan& p, const ss_options& o, const PeerTier* peer) {
@@ -497,7 +515,30 @@ class CudaMover final : public Mover {
     return async_->begin(key, block_host(block));
   }
   uint64_t read_end(void* h) override { return async_ && h ? async_->end(h) : 0; }
-  bool read_done(void* h) override { return !async_ || !h || async_->done(h); }
+  bool read_done(void* h) override {
+    if (!async_ || !h) return true;
+    if (deterministic_) {  // the reference's immediate transport: every read complete when asked
+      async_->wait(h);
+      return true;
+    }
+    return async_->done(h);
+  }
+  // Landing reads: on the pool behind the demand reads (whole-unit reads), or the synchronous read with one reader.
+  void* read_landing_begin(uint32_t key, int32_t block) override {
+    if (!async_) {
+      read_unit(key, block);
+      return nullptr;
+    }
+    return async_->begin_landing(key, block_host(block));
+  }
+  uint64_t read_landing_end(void* h, LandingEnd* end) override {
+    *end = LandingEnd{};
+    return read_end(h);
+  }
+  bool read_landing_cancel(void* h, LandingEnd* end) noexcept override {
+    *end = LandingEnd{};
+    return async_ && h && !deterministic_ && async_->cancel(h);  // (immediate reads: nothing left to cancel)
+  }
   void h2h(int32_t src, int32_t dst, uint32_t key) override {
     if (peer_ && peer_->owned(key)) return;
     std::memcpy(block_host(dst), block_host(src), size_t(x_.unit_bytes));
@@ -1340,7 +1381,8 @@ class CudaDgContext final : public DgContext {
   // peer store or its pinned block; false when its only copy is its file.
   bool live_copy(uint32_t k, std::vector<char>& out) {
     const SlotCache::Home home = core_->home(k);
-    if (home == SlotCache::Home::File) return false;
+    if (home == SlotCache::Home::File || home == SlotCache::Home::Landing || home == SlotCache::Home::Landed)
+      return false;  // (only its file is a unit's own copy)
     out.resize(size_t(x_.unit_bytes));
     const int32_t slot = core_->slot_of(k);
     if (slot >= 0 && (home == SlotCache::Home::Device || home == SlotCache::Home::Evicting)) {
@@ -1585,6 +1627,18 @@ class CudaDgContext final : public DgContext {
     s.pf_revert_bytes = d(c.pf_revert_bytes, base_.pf_revert_bytes);
     s.pf_strict_refused = d(c.pf_strict_refused, base_.pf_strict_refused);
     s.bank_kept = d(c.bank_kept, base_.bank_kept);
+    s.landing_issued = d(c.landing_issued, base_.landing_issued);
+    s.landing_promoted = d(c.landing_promoted, base_.landing_promoted);
+    s.landing_late = d(c.landing_late, base_.landing_late);
+    s.landing_wait_ns = d(c.landing_wait_ns, base_.landing_wait_ns);
+    s.landing_expired = d(c.landing_expired, base_.landing_expired);
+    s.landing_dropped_full = d(c.landing_dropped_full, base_.landing_dropped_full);
+    s.landing_read_bytes = d(c.landing_read_bytes, base_.landing_read_bytes);
+    s.landing_cancelled = d(c.landing_cancelled, base_.landing_cancelled);
+    s.landing_expired_layer = d(c.landing_expired_layer, base_.landing_expired_layer);
+    s.landing_skipped_passed = d(c.landing_skipped_passed, base_.landing_skipped_passed);
+    s.landing_yields = d(c.landing_yields, base_.landing_yields);
+    s.landing_aborted_bytes = d(c.landing_aborted_bytes, base_.landing_aborted_bytes);
     s.disk_queue_resolved = x_.disk_queue;
     s.disk_depth_adapt = adapt_;  // (properties of the open's controller since open / reset_open)
     s.disk_depth_active = x_.disk_tier ? x_.disk_queue : 0;
@@ -1695,8 +1749,24 @@ class CudaDgContext final : public DgContext {
                   (unsigned long long)check_repaired_, check_wait_s_);
     require(len > 0 && size_t(len) < sizeof buf, SS_E_BACKEND, "device-gated: the stats text does not fit its buffer");
     std::string out(buf);
-    out.pop_back();  // the closing brace: the read depth's section follows
+    out.pop_back();  // the closing brace: the read depth's and the landings' sections follow
     out += adapt_json();
+    if (x_.L) {
+      char b[768];
+      std::snprintf(b, sizeof b,
+                    ",\"landing\":{\"blocks\":%u,\"ttl\":%u,\"max_queued\":%u,\"chunk\":%u,\"issued\":%llu,"
+                    "\"promoted\":%llu,\"late\":%llu,\"wait_ns\":%llu,\"expired\":%llu,\"dropped_full\":%llu,"
+                    "\"read_bytes\":%llu,\"failed\":%llu,\"cancelled\":%llu,\"expired_layer\":%llu,"
+                    "\"skipped_passed\":%llu,\"units\":%u}",
+                    x_.L, x_.landing_ttl, x_.landing_queued, x_.landing_chunk, (unsigned long long)s.landing_issued,
+                    (unsigned long long)s.landing_promoted, (unsigned long long)s.landing_late,
+                    (unsigned long long)s.landing_wait_ns, (unsigned long long)s.landing_expired,
+                    (unsigned long long)s.landing_dropped_full, (unsigned long long)s.landing_read_bytes,
+                    (unsigned long long)(core_->stats().landing_failed - base_.landing_failed),
+                    (unsigned long long)s.landing_cancelled, (unsigned long long)s.landing_expired_layer,
+                    (unsigned long long)s.landing_skipped_passed, core_->landing_units());
+      out += b;
+    }
     out += '}';
     return out;
   }
@@ -2044,7 +2114,7 @@ class CudaDgContext final : public DgContext {
     const uint64_t per_chunk = std::max<uint64_t>(1, (uint64_t(1) << 30) / hs);
     std::vector<uint64_t> chunk_units;
     std::vector<size_t> chunk_bytes;
-    for (uint64_t left = peer_ && peer_->all_owned ? 0 : uint64_t(x_.blocks) + x_.S; left > 0;) {
+    for (uint64_t left = peer_ && peer_->all_owned ? 0 : uint64_t(x_.blocks) + x_.S + x_.L; left > 0;) {
       chunk_units.push_back(std::min(per_chunk, left));
       chunk_bytes.push_back(size_t(chunk_units.back() * hs));
       left -= chunk_units.back();
@@ -2129,6 +2199,8 @@ class CudaDgContext final : public DgContext {
     c.pf_revert = o_.dg_pf_revert_unused != 0;
     c.pf_strict = o_.dg_pf_strict_admit != 0;
     c.bank_keep = o_.dg_bank_keep;  // (0..2; no effect without the file tier or with dg_no_admit)
+    c.landing_blocks = x_.L;        // (after the staging buffers: block indices blocks + S ..)
+    c.landing_ttl = x_.landing_ttl;
     if (x_.disk_tier) {  // a file miss: the unit's parts from their files, checked against the descriptor's hash
       unsigned n = 8;
       if (const char* e = std::getenv("TSB_FILE_READERS")) n = unsigned(std::max(1L, std::min(64L, std::atol(e))));
@@ -2147,12 +2219,14 @@ class CudaDgContext final : public DgContext {
           read_checked(x_.gated[g], int(key - x_.unit_base[g]), dst, flight_pools_[worker].get());
         });
         mover_->set_async(async_.get());
+        async_->set_landing(x_.landing_queued, x_.landing_chunk != 0);
       }
       // dg_disk_queue_adapt: the pool's demand reads at a measured depth (1 or the resolved queue); declined where
       // the pool is not demand-only over several readers
       if (o_.dg_disk_queue_adapt) {
         adapt_ = 2;
         if (!async_) adapt_why_ = "one reader";
+        else if (x_.L) adapt_why_ = "landing blocks";
         else if (o_.dg_disk_prefetch) adapt_why_ = "file prefetches";
         else adapt_ = 1;
       }
@@ -2524,7 +2598,7 @@ std::vector<uint64_t> dg_layout_summary(const Desc& d, const Plan& p, const ss_o
   if (residents) *residents = x.residents;
   return {x.keys, x.R, x.D, x.B, x.P, x.Q, x.I, x.F, x.S, x.disk_queue, x.blocks, x.persistent_slots, x.slots,
           x.guard_slot, x.unit_bytes, x.host_stride, x.disk_tier, x.disk_prefetch, x.scored, x.w_trans, x.w_freq,
-          x.w_rec, x.residents.size()};
+          x.w_rec, x.residents.size(), x.L, x.landing_queued, x.landing_ttl, x.landing_chunk};
 }
 
 std::unique_ptr<DgContext> open_dg_context(const Desc& d, const Plan& p, const ss_options& o, const PeerTier* peer) {

@@ -129,11 +129,62 @@ AsyncReads::~AsyncReads() {
   {
     std::lock_guard<std::mutex> lk(mu_);
     stop_ = true;
+    for (Job* j : land_q_) delete j;  // landing reads never started are dropped
+    land_q_.clear();
   }
   cv_.notify_all();
   for (std::thread& t : th_) t.join();
   for (Job* j : running_) delete j;
   for (size_t i = head_; i < q_.size(); ++i) delete q_[i];
+}
+
+void AsyncReads::set_landing(unsigned cap, bool reserve) {
+  std::lock_guard<std::mutex> lk(mu_);
+  land_cap_ = std::max(1u, cap);
+  land_reserve_ = reserve;
+}
+
+bool AsyncReads::landing_ready() const {
+  if (land_q_.empty() || head_ < q_.size()) return false;
+  if (!land_reserve_) return reading_ < land_cap_;
+  const unsigned readers = unsigned(th_.size());
+  if (readers == 1) return reading_ == 0;
+  return landing_running_ < land_cap_ && landing_running_ + 1 < readers;
+}
+
+void* AsyncReads::begin_landing(uint32_t key, char* dst) {
+  Job* j = new Job;
+  j->key = key;
+  j->dst = dst;
+  j->landing = true;
+  {
+    std::lock_guard<std::mutex> lk(mu_);
+    land_q_.push_back(j);
+  }
+  cv_.notify_one();
+  return j;
+}
+
+bool AsyncReads::cancel(void* h) {
+  std::lock_guard<std::mutex> lk(mu_);
+  const auto it = std::find(land_q_.begin(), land_q_.end(), static_cast<Job*>(h));
+  if (it == land_q_.end()) return false;  // running or finished: ended as usual
+  delete *it;
+  land_q_.erase(it);
+  return true;
+}
+
+void AsyncReads::wait(void* h) {
+  Job* j = static_cast<Job*>(h);
+  std::unique_lock<std::mutex> lk(mu_);
+  const auto queued = std::find(land_q_.begin(), land_q_.end(), j);
+  if (queued != land_q_.end()) {  // a landing read not started: it runs now, at the front of the demand reads
+    land_q_.erase(queued);
+    j->landing = false;
+    q_.insert(q_.begin() + std::ptrdiff_t(head_), j);
+    cv_.notify_one();
+  }
+  done_cv_.wait(lk, [&] { return j->done.load(std::memory_order_acquire); });
 }
 
 void* AsyncReads::begin(uint32_t key, char* dst) {
@@ -152,9 +203,9 @@ bool AsyncReads::done(void* h) const { return static_cast<const Job*>(h)->done.l
 
 uint64_t AsyncReads::end(void* h) {
   Job* j = static_cast<Job*>(h);
+  wait(h);
   {
     std::unique_lock<std::mutex> lk(mu_);
-    done_cv_.wait(lk, [&] { return j->done.load(std::memory_order_acquire); });
     auto it = std::find(running_.begin(), running_.end(), j);
     require(it != running_.end(), SS_E_BACKEND, "a file read ended twice");
     running_.erase(it);
@@ -169,13 +220,22 @@ void AsyncReads::loop(unsigned worker) {
     Job* j = nullptr;
     {
       std::unique_lock<std::mutex> lk(mu_);
-      // (stopping drains the queue without the depth limit)
-      cv_.wait(lk, [&] { return (stop_ || reading_ < limit_) && (head_ < q_.size() || stop_); });
-      if (head_ == q_.size()) return;  // (stopping with nothing queued)
-      j = q_[head_++];
-      if (head_ == q_.size()) {  // the queue's storage reused once every job was taken
-        q_.clear();
-        head_ = 0;
+      // (stopping drains the demand queue without the depth limit; landing reads never started are dropped)
+      cv_.wait(lk, [&] {
+        return ((stop_ || reading_ < limit_) && (head_ < q_.size() || stop_)) || (!stop_ && landing_ready());
+      });
+      if (head_ < q_.size() && (stop_ || reading_ < limit_)) {
+        j = q_[head_++];
+        if (head_ == q_.size()) {  // the queue's storage reused once every job was taken
+          q_.clear();
+          head_ = 0;
+        }
+      } else if (!stop_ && landing_ready()) {
+        j = land_q_.front();
+        land_q_.erase(land_q_.begin());
+        ++landing_running_;
+      } else {
+        return;  // (stopping with nothing queued)
       }
       running_.push_back(j);
       ++reading_;
@@ -198,6 +258,7 @@ void AsyncReads::loop(unsigned worker) {
       std::lock_guard<std::mutex> lk(mu_);
       j->done.store(true, std::memory_order_release);
       --reading_;
+      landing_running_ -= j->landing ? 1 : 0;
       if (depth_ && busy_) {
         ++busy_reads_;
         if (reading_ == 0 && head_ == q_.size()) {  // idle again: the period measured, the next depth set
@@ -208,10 +269,10 @@ void AsyncReads::loop(unsigned worker) {
           limit_ = std::min(std::max(d, 1u), unsigned(th_.size()));
         }
       }
-      more = head_ < q_.size();
+      more = head_ < q_.size() || !land_q_.empty();
     }
     done_cv_.notify_all();
-    if (more) cv_.notify_one();  // (a read held back by the depth may start)
+    if (more) cv_.notify_all();  // (a read held back by the depth, the cap or the reserve may start)
   }
 }
 

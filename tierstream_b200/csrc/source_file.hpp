@@ -33,7 +33,16 @@ class AsyncReads {
   AsyncReads& operator=(const AsyncReads&) = delete;
   void* begin(uint32_t key, char* dst);
   bool done(void* h) const;
+  void wait(void* h);  // until the read finished (it is still ended with end)
   uint64_t end(void* h);
+  // Landing reads (dg_landing_blocks): queued behind every demand read; a reader takes one only while no demand read
+  // is queued and, with `reserve`, fewer than `cap` landing reads run and one reader stays free of them (a single
+  // reader: only while nothing else runs), else while fewer than `cap` reads of either kind run. Landing reads are
+  // whole-unit reads here. cancel drops one that has not started (true: the handle is gone); ending one still queued
+  // moves it to the front of the demand reads first.
+  void set_landing(unsigned cap, bool reserve);
+  void* begin_landing(uint32_t key, char* dst);
+  bool cancel(void* h);
   // dg_disk_queue_adapt: reads start only while fewer than the controller's depth run (the readers stay allocated),
   // and each busy period of the pool (from idle to idle) is measured and fed to it, each read counted as
   // unit_bytes. Set while idle (the open, reset_open); nullptr: every reader.
@@ -51,7 +60,9 @@ class AsyncReads {
     std::atomic<bool> done{false};
     std::exception_ptr err;
     uint64_t ns = 0;
+    bool landing = false;
   };
+  bool landing_ready() const;  // (under mu_) a reader may take the oldest landing read
   void loop(unsigned worker);
   std::function<void(uint32_t, char*, unsigned)> read_;
   mutable std::mutex mu_;
@@ -62,6 +73,9 @@ class AsyncReads {
   std::vector<std::thread> th_;
   bool stop_ = false;
   unsigned reading_ = 0;                   // reads taken and not finished
+  std::vector<Job*> land_q_;               // landing reads not started, oldest first (owned)
+  unsigned landing_running_ = 0, land_cap_ = 1;
+  bool land_reserve_ = false;
   unsigned limit_ = 0;                     // reads allowed at once (the readers, or the controller's depth)
   std::unique_ptr<ReadDepth> depth_;       // dg_disk_queue_adapt's controller (or none)
   uint64_t unit_bytes_ = 0;

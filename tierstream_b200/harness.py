@@ -20,7 +20,7 @@ class DgSetup:
                  host_spare_units=None, diag=False, test_hooks=True, wb_defer=1, wb_stream=1, verify=False,
                  timeout_ms=10000, device_bytes=None, resident_order=None, inclusive=0, disk_keys=(), disk_staging=0,
                  disk_prefetch=0, disk_queue=0, policy=0, weights=None, profile=None, bank_keep=0,
-                 disk_queue_adapt=0):
+                 disk_queue_adapt=0, landing_blocks=0, landing_ttl=0):
         G, U = model.layers, model.units
         tiers = [abi.SS_TIER_PINNED] * (G * U)
         if resident_keys is None:
@@ -47,7 +47,7 @@ class DgSetup:
         b.host_spare_units = host_spare_units if host_spare_units is not None else spare_per_layer * G + inclusive
         hs = (unit + 4095) // 4096 * 4096
         b.host_pinned_bytes = (G * U - len(resident_keys) - len(self.disk_keys) + b.host_spare_units + 2 +
-                               ((disk_staging or 8) if self.disk_keys else 0)) * hs + (64 << 20)
+                               ((disk_staging or 8) + landing_blocks if self.disk_keys else 0)) * hs + (64 << 20)
         self.desc = runtime.Desc(model.desc())
         self.plan = runtime.Plan(self.desc, b, tiers=tiers)
         o = abi.options_defaults()
@@ -75,6 +75,7 @@ class DgSetup:
             o.dg_disk_queue = disk_queue
             o.dg_bank_keep = bank_keep  # bank-served file reads kept in pinned blocks (1: recency front, 2: middle)
             o.dg_disk_queue_adapt = disk_queue_adapt  # (with disk_queue SS_DG_DISK_QUEUE_AUTO)
+            o.dg_landing_blocks, o.dg_landing_ttl = landing_blocks, landing_ttl  # (predictions land file units)
         self.budget, self.options = b, o
 
 
