@@ -241,6 +241,10 @@ SS_API ss_status tsb_test_score_profile(const ss_desc* d, const void* profile, u
  * verdicts, calibrating (0 / 1). verdicts[16][7] (may be NULL), the last ones, oldest first: number, reads before it,
  * depth from, depth to, mean rate at U, mean rate at 1 (bytes / ns), reason (0 start, 1 keep U, 2 keep 1, 3 split,
  * 4 recheck, 5 drift); *n_verdicts = how many are filled. */
+/* Test hook of the reads-in-flight pool: its scheduling rules checked with a fake read (landing reads behind demand
+ * reads, the landing cap and reader reserve, cancel of a landing read not started only, a demand's end running a
+ * queued landing read first). SS_OK, or SS_E_BACKEND naming the rule broken. No file, no device. */
+SS_API ss_status tsb_test_read_pool(void);
 SS_API ss_status tsb_test_read_depth(uint32_t bound, const double* params, uint32_t n, const uint64_t* reads,
                                      const uint64_t* bytes, const uint64_t* ns, uint32_t* depth, uint64_t* counters,
                                      double* verdicts, uint32_t* n_verdicts);

@@ -15,6 +15,10 @@
 #include "peer.hpp"
 #include "plan.hpp"
 #include "read_depth.hpp"
+
+namespace tsb {
+void check_read_pool();  // read_pool_check.cpp
+}
 #include "resident_set.hpp"
 #include "score_profile.hpp"
 #include "strix_stream/ss.h"
@@ -748,6 +752,10 @@ ss_status tsb_test_sha256(const void* data, uint64_t len, uint8_t* out) {
     const std::string h = tsb::sha256(data, size_t(len));
     std::memcpy(out, h.data(), 32);
   });
+}
+
+ss_status tsb_test_read_pool(void) {
+  return guard([] { tsb::check_read_pool(); });
 }
 
 ss_status tsb_test_read_depth(uint32_t bound, const double* params, uint32_t n, const uint64_t* reads,
