@@ -86,6 +86,24 @@ def test_file_tier_with_reads_in_flight_under_concurrency(seed):
     every_routed_read(cfg, ids, reads)
 
 
+@pytest.mark.parametrize("seed", range(16))
+def test_landings_and_bank_keep_under_concurrency(seed):
+    """Landing blocks (predictions of file units read ahead, promoted by demands, expired by layer or TTL) and bank
+    keep (bank-served file reads into the pinned blocks that become their homes), with reads landing late: every
+    routed unit's bytes are its own and no hazard is seen."""
+    r = np.random.default_rng(9100 + seed)
+    G, U = int(r.integers(2, 6)), int(r.choice([8, 16]))
+    B = int(r.choice([2, 4]))
+    kw = dict(G=G, U=U, R=1, pinned=int(r.integers(0, U // 2)), D=int(r.integers(1, 3)), B=B, S=int(r.integers(2, 5)),
+              Q=int(r.integers(0, G + 1)), tokens=25, s=float(r.choice([0.8, 1.2])), seed=int(r.integers(0, 1000)),
+              n_pred=int(r.integers(1, B + 1)), landing_blocks=int(r.integers(1, 12)),
+              landing_ttl=int(r.choice([0, 1, 3])), disk_queue=int(r.integers(2, 5)),
+              bank_keep=int(r.integers(0, 3)), wb_defer=int(r.integers(0, 2)))
+    cfg, ids, preds = make_disk_case(**kw)
+    reads = run_async(cfg, ids, preds, 9500 + seed, int(r.choice([0, 40, 150])))
+    every_routed_read(cfg, ids, reads)
+
+
 @pytest.mark.parametrize("reset_at", [7, 15])
 def test_reset_mid_trace_under_concurrency(reset_at):
     cfg, ids, preds = make_disk_case(G=5, U=16, R=3, pinned=5, D=2, B=3, Q=12, S=3, tokens=30, s=0.9, seed=5,

@@ -400,11 +400,15 @@ void dg_async_replay(const tsb_dg_replay_config* c, const int32_t* ids, const in
   cfg.clean_evict = c->clean_evict != 0;
   cfg.pf_revert = c->pf_revert != 0;
   cfg.pf_strict = c->pf_strict != 0;
+  cfg.bank_keep = c->bank_keep;
+  cfg.landing_blocks = c->landing_blocks;
+  cfg.landing_ttl = c->landing_ttl;
   const uint32_t G = c->n_gated;
   uint32_t keys = 0;
   for (uint32_t g = 0; g < G; ++g) keys += c->n_units[g];
   AsyncMover m(std::vector<uint64_t>(c->part_bytes, c->part_bytes + c->n_parts), keys,
-               c->persistent_slots + 2 * c->bank_slots + 1, c->blocks + c->disk_staging, G, src_units, seed, delay_us);
+               c->persistent_slots + 2 * c->bank_slots + 1, c->blocks + c->disk_staging + c->landing_blocks, G,
+               src_units, seed, delay_us);
   auto core = std::make_unique<SlotCache>(cfg, &m);
   core->set_mutation(mutation);  // a planted ordering fault (the entry before its bytes, a demand not covered)
   std::vector<uint32_t> order(c->order, c->order + c->n_order);
