@@ -332,6 +332,13 @@ SS_API ss_status tsb_peer_store_create_striped(const ss_desc* d, const int32_t* 
 SS_API ss_status tsb_peer_tier_verify(const ss_desc* d, const tsb_peer_tier* peer, int device,
                                       uint64_t* checked_units);
 
+/* Test hook of the striped layout: the copies one owned unit's miss issues on `rank` of `world` (the layout the
+ * mover uses: a stripe from every GPU, the next rank's first, each split at the part boundaries it crosses), for a
+ * unit of n_parts parts of part_bytes[] bytes; each copy as 5 values: source rank, offset in that rank's stripe,
+ * part, offset in the part, bytes. Up to cap copies are written; *n = how many there are. No device. */
+SS_API ss_status tsb_test_peer_pieces(const uint64_t* part_bytes, uint32_t n_parts, uint32_t world, int32_t rank,
+                                      uint64_t* copies, uint32_t cap, uint32_t* n);
+
 /* A re-plan (after a new all-reduce of routing counts and tsb_peer_plan): dst, allocated by tsb_peer_store_alloc for
  * the new owners, is filled with its units from where they live now (old_owner, old_base[world]: every rank's current
  * store as seen from this process), by the land kernel on `stream` (peers over NVLink, this rank's own store in HBM);

@@ -213,3 +213,44 @@ def test_a_rank_that_leaves_fails_the_exchange_with_an_error(tmp_path):
     assert ctx.processes[1].exitcode == 3
     text = (tmp_path / "r0.txt").read_text()
     assert text.startswith("raised:") and text.endswith(" 16"), text
+
+
+def _pieces(parts, world, rank):
+    lib = abi.load()
+    pb = (C.c_uint64 * len(parts))(*parts)
+    cap = world + len(parts) + 4
+    out = np.zeros((cap, 5), dtype=np.uint64)
+    n = C.c_uint32()
+    assert lib.tsb_test_peer_pieces(pb, len(parts), world, rank, out.ctypes.data_as(C.POINTER(C.c_uint64)), cap,
+                                    C.byref(n)) == abi.SS_OK
+    assert n.value <= cap
+    return out[:n.value]
+
+
+@pytest.mark.parametrize("seed", range(40))
+def test_striped_miss_copies_cover_the_unit(seed):
+    """The copies a striped miss issues (the mover's own split, tsb_test_peer_pieces): every byte of every part
+    exactly once, each from the stripe that holds it and inside it, the stripes in rotation from the next rank to this
+    rank's own, at most world + parts - 1 copies."""
+    r = np.random.default_rng(3000 + seed)
+    parts = [int(r.integers(1, 40)) * 256 + (int(r.integers(0, 256)) if seed % 4 == 3 else 0)
+             for _ in range(int(r.integers(1, 5)))]
+    unit = sum(parts)
+    offset = np.cumsum([0] + parts[:-1])
+    for world in (1, 2, 3, 5, 8):
+        s = peer.stripe_bytes(unit, world)
+        for rank in range(world):
+            cp = _pieces(parts, world, rank)
+            assert len(cp) <= world + len(parts) - 1
+            covered = [np.zeros(p, dtype=np.int32) for p in parts]
+            order = []
+            for src, in_stripe, part, in_part, n in (tuple(int(v) for v in row) for row in cp):
+                assert n > 0 and in_stripe + n <= peer.stripe_range(unit, world, src)[1]
+                assert src * s + in_stripe == offset[part] + in_part  # the same unit bytes on both sides
+                covered[part][in_part:in_part + n] += 1
+                if not order or order[-1] != src:
+                    order.append(src)
+            assert all((c == 1).all() for c in covered), "a byte copied twice or never"
+            stripes = [q for q in range(world) if peer.stripe_range(unit, world, q)[1] > 0]
+            want = [(rank + j) % world for j in range(1, world + 1) if (rank + j) % world in stripes]
+            assert order == want, (order, want)

@@ -856,6 +856,41 @@ ss_status tsb_peer_unmap(void* base) {
   return guard([&] { tsb::ipc_unmap(base); });
 }
 
+ss_status tsb_test_peer_pieces(const uint64_t* part_bytes, uint32_t n_parts, uint32_t world, int32_t rank,
+                               uint64_t* copies, uint32_t cap, uint32_t* n) {
+  return guard([&] {
+    need(part_bytes && n_parts && n && (copies || !cap), "tsb_test_peer_pieces: null argument");
+    need(world >= 1 && rank >= 0 && uint32_t(rank) < world, "tsb_test_peer_pieces: rank outside [0, world)");
+    const std::vector<uint64_t> bytes_of(part_bytes, part_bytes + n_parts);
+    std::vector<uint64_t> offset(n_parts);
+    uint64_t unit = 0;
+    for (uint32_t p = 0; p < n_parts; ++p) {
+      offset[p] = unit;
+      unit += part_bytes[p];
+    }
+    tsb::PeerTier t;  // one owned key at position 0 of every store, stores at fake addresses r << 40
+    t.world = world;
+    t.rank = rank;
+    t.layout = tsb::kStriped;
+    t.stripe = tsb::stripe_bytes(unit, world);
+    t.owner = {0};
+    t.index = {0};
+    for (uint32_t r = 0; r < world; ++r) t.base.push_back(reinterpret_cast<char*>(uintptr_t(r + 1) << 40));
+    uint32_t at = 0;
+    t.pieces(0, unit, [&](const char* src, uint64_t off, uint64_t bytes, int32_t from) {
+      const uint64_t in_stripe = uint64_t(reinterpret_cast<uintptr_t>(src) - (uintptr_t(from + 1) << 40));
+      tsb::split_parts(offset, bytes_of, off, bytes, [&](uint32_t p, uint64_t a, uint64_t len) {  // the mover's split
+        if (at < cap) {
+          const uint64_t row[5] = {uint64_t(from), in_stripe + (a - off), p, a - offset[p], len};
+          std::memcpy(copies + size_t(at) * 5, row, sizeof row);
+        }
+        ++at;
+      });
+    });
+    *n = at;
+  });
+}
+
 uint64_t tsb_peer_stripe_bytes(uint64_t unit_bytes, uint32_t world) {
   return world ? tsb::stripe_bytes(unit_bytes, world) : 0;
 }

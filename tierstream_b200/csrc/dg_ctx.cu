@@ -868,10 +868,7 @@ class CudaMover final : public Mover {
   // f(part, unit offset, bytes) for each part that [off, off + n) of the unit's bytes overlaps
   template <class F>
   void for_parts(uint64_t off, uint64_t n, F&& f) const {
-    for (uint32_t p = 0; p < parts(); ++p) {
-      const uint64_t a = std::max(off, x_.part_offset[p]), b = std::min(off + n, x_.part_offset[p] + x_.part_bytes[p]);
-      if (a < b) f(p, a, b - a);
-    }
+    split_parts(x_.part_offset, x_.part_bytes, off, n, f);
   }
   char* block_dev(int32_t b) const { return b < 0 ? b_.staging_d : b_.blocks_d[size_t(b)]; }
   char* block_host(int32_t b) const { return b < 0 ? b_.staging : b_.blocks[size_t(b)]; }

@@ -55,6 +55,17 @@ inline uint64_t stripe_len(uint64_t unit_bytes, uint64_t stripe, uint32_t r) {
 // unowned keys.
 std::vector<int64_t> striped_index(const std::vector<int32_t>& owner, uint64_t* owned);
 
+// f(part, unit offset, bytes) for each part that [off, off + n) of a unit's bytes overlaps (parts back to back at
+// part_offset[p], part_bytes[p] long): how one piece of a unit is split into copies into the arena's part slots.
+template <class F>
+void split_parts(const std::vector<uint64_t>& part_offset, const std::vector<uint64_t>& part_bytes, uint64_t off,
+                 uint64_t n, F&& f) {
+  for (uint32_t p = 0; p < part_bytes.size(); ++p) {
+    const uint64_t a = std::max(off, part_offset[p]), b = std::min(off + n, part_offset[p] + part_bytes[p]);
+    if (a < b) f(p, a, b - a);
+  }
+}
+
 struct PeerTier {
   uint32_t world = 0;
   int32_t rank = -1;
