@@ -104,6 +104,29 @@ def test_landings_and_bank_keep_under_concurrency(seed):
     every_routed_read(cfg, ids, reads)
 
 
+@pytest.mark.parametrize("seed", range(12))
+def test_every_file_tier_option_together_under_concurrency(seed):
+    """Landings, bank keep, clean evict, reverts, strict admission, scoring and rounds at once, with reads in flight
+    landing late: every routed unit's bytes are its own and no hazard is seen."""
+    r = np.random.default_rng(9900 + seed)
+    G, U = int(r.integers(3, 6)), int(r.choice([8, 16]))
+    B = int(r.choice([2, 4]))
+    kw = dict(G=G, U=U, R=1, pinned=int(r.integers(1, U // 2)), D=2, B=B, S=int(r.integers(2, 5)), Q=int(r.integers(1, G + 1)),
+              tokens=25, s=float(r.choice([0.8, 1.2])), seed=int(r.integers(0, 1000)), n_pred=int(r.integers(1, B + 1)),
+              disk_prefetch=int(r.integers(0, 2)), landing_blocks=int(r.integers(1, 8)),
+              landing_ttl=int(r.choice([0, 2])), disk_queue=int(r.integers(2, 5)), bank_keep=int(r.integers(1, 3)),
+              clean_evict=1, pf_revert=int(r.integers(0, 2)), pf_strict=int(r.integers(0, 2)),
+              policy=int(r.integers(0, 3)), round_every=int(r.choice([0, 4])), wb_defer=int(r.integers(0, 2)))
+    cfg, ids, preds = make_disk_case(**kw)
+    try:
+        reads = run_async(cfg, ids, preds, 9950 + seed, int(r.choice([0, 40, 150])))
+    except AssertionError as e:
+        if "capacity" in str(e).lower() or "no free slot" in str(e).lower():
+            pytest.skip("a configuration the cache refuses: %s" % e)
+        raise
+    every_routed_read(cfg, ids, reads)
+
+
 @pytest.mark.parametrize("reset_at", [7, 15])
 def test_reset_mid_trace_under_concurrency(reset_at):
     cfg, ids, preds = make_disk_case(G=5, U=16, R=3, pinned=5, D=2, B=3, Q=12, S=3, tokens=30, s=0.9, seed=5,
