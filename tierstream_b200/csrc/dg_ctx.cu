@@ -176,7 +176,7 @@ void check_dg_options(const ss_budget& b, const ss_options& o, const PeerTier* p
     if (f.first > 1) dg_refuse(SS_E_INVALID, std::string(f.second) + " must be 0 or 1");
   if (o.dg_disk_tier && peer) dg_refuse(SS_E_UNSUPPORTED, "the file tier with the peer tier is not in this build");
   if (o.dg_prior_len)
-    dg_refuse(SS_E_UNSUPPORTED, "an opt-in device-gated policy of the reference that is not in this build is set");
+    dg_refuse(SS_E_UNSUPPORTED, "dg_prior_len (window prefetch priors) is not in this build");
 }
 
 // The gated layers (every layer with units; each must be streamable) and the one part shape they share: the arena
