@@ -107,9 +107,9 @@ def args_():
                         "line then names the layer count; not the config's number)")
     p.add_argument("--peer-layout", default="auto", choices=["auto", "whole", "striped"],
                    help="peer tier stores: whole units at their owners, every unit striped over all GPUs (a miss "
-                        "reads a stripe from each), or auto (the default): striped for the Mixtral shape (1,959 "
-                        "against 1,723 GB/s for whole units at 4 GPUs, 1,222 against 1,156 at 2), whole units for the "
-                        "top-8 shapes (measured that way)")
+                        "reads a stripe from each), or auto (the default): striped for the Mixtral shape (3,537 "
+                        "against 2,950 GB/s for whole units at 8 GPUs, 1,959 against 1,723 at 4, 1,222 against 1,156 "
+                        "at 2), whole units for the top-8 shapes (measured that way)")
     p.add_argument("--peer-copy", default="auto", choices=["auto", "kernel", "ce"],
                    help="peer tier mover: the copy engines, the land kernel's SM loads, or auto (the default): the "
                         "land kernel for striped stores (it pulls every stripe at once; one copy-engine stream takes "
